@@ -1,0 +1,181 @@
+"""ctypes binding of ``libhx_b200.so`` (declarations in include/heliox_b200.h).
+
+There is no fallback: if the native library or a CUDA device is missing, the
+calls raise.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "libhx_b200.so")
+
+_dp = C.POINTER(C.c_double)
+_ip = C.POINTER(C.c_int)
+_fp = C.POINTER(C.c_float)
+
+HX_P = {
+    "hh.gnabar": 0,
+    "hh.gkbar": 1,
+    "hh.gl": 2,
+    "hh.el": 3,
+    "pas.g": 4,
+    "pas.e": 5,
+    "cm": 6,
+    "IClamp.amp": 7,
+}
+HX_P_COUNT = 8
+
+
+class GroupDesc(C.Structure):
+    _fields_ = [
+        ("ncell", C.c_int),
+        ("nnode", C.c_int),
+        ("parent", _ip),
+        ("a", _dp),
+        ("b", _dp),
+        ("area", _dp),
+        ("cm", _dp),
+        ("celsius", C.c_double),
+        ("dt", C.c_double),
+        ("nhh", C.c_int),
+        ("hh_node", _ip),
+        ("hh_gnabar", _dp),
+        ("hh_gkbar", _dp),
+        ("hh_gl", _dp),
+        ("hh_el", _dp),
+        ("hh_ena", _dp),
+        ("hh_ek", _dp),
+        ("npas", C.c_int),
+        ("pas_node", _ip),
+        ("pas_g", _dp),
+        ("pas_e", _dp),
+        ("nic", C.c_int),
+        ("ic_node", _ip),
+        ("ic_del", _dp),
+        ("ic_dur", _dp),
+        ("ic_amp", _dp),
+    ]
+
+
+class PlanStats(C.Structure):
+    _fields_ = [
+        ("npack", C.c_int),
+        ("max_pack_nodes", C.c_int),
+        ("max_pack_hh", C.c_int),
+        ("max_levels", C.c_int),
+        ("max_crit_nodes", C.c_int),
+        ("nbranch", C.c_int),
+        ("imbalance", C.c_double),
+        ("smem_fwd", C.c_size_t),
+        ("smem_bwd", C.c_size_t),
+    ]
+
+    def as_dict(self):
+        return {k: getattr(self, k) for k, _ in self._fields_}
+
+
+# name -> (restype, argtypes)
+SIGNATURES = {
+    "hx_abi_version": (C.c_int, []),
+    "hx_create": (C.c_int, [C.POINTER(C.c_void_p), C.c_int]),
+    "hx_destroy": (C.c_int, [C.c_void_p]),
+    "hx_last_error": (C.c_char_p, [C.c_void_p]),
+    "hx_set_stream": (C.c_int, [C.c_void_p, C.c_void_p]),
+    "hx_set_pack_target": (C.c_int, [C.c_void_p, C.c_int]),
+    "hx_set_tape_budget": (C.c_int, [C.c_void_p, C.c_size_t]),
+    "hx_load_group": (C.c_int, [C.c_void_p, C.POINTER(GroupDesc)]),
+    "hx_get_plan_stats": (C.c_int, [C.c_void_p, C.POINTER(PlanStats)]),
+    "hx_plan_check": (C.c_int, [C.POINTER(GroupDesc), C.c_int, C.POINTER(PlanStats), _dp]),
+    "hx_set_param": (C.c_int, [C.c_void_p, C.c_int, _dp, C.c_int]),
+    "hx_get_param": (C.c_int, [C.c_void_p, C.c_int, _dp, C.c_int]),
+    "hx_simulate": (C.c_int, [C.c_void_p, C.c_int, C.c_double, C.c_int, _ip, _dp]),
+    "hx_forward_capture": (C.c_int, [C.c_void_p, C.c_int, C.c_double, C.c_int, _ip, _dp]),
+    "hx_forward_capture_dev": (C.c_int, [C.c_void_p, C.c_int, C.c_double, C.c_int, _ip, C.c_void_p]),
+    "hx_backward": (C.c_int, [C.c_void_p, _dp, C.POINTER(_dp)]),
+    "hx_backward_dev": (C.c_int, [C.c_void_p, C.c_void_p, C.POINTER(C.c_void_p)]),
+    "hx_reduce_grads_f32": (C.c_int, [C.c_void_p, C.c_int, _ip, _ip, _ip, _fp, _fp, C.c_int]),
+    "hx_last_kernel_ms": (C.c_int, [C.c_void_p, C.c_int, _dp, _ip]),
+}
+
+_LIB = None
+
+
+def load(path: str = LIB_PATH):
+    """Load the native library (raises if it has not been built)."""
+    global _LIB
+    if _LIB is not None:
+        return _LIB
+    if not os.path.exists(path):
+        raise RuntimeError(f"heliox_b200 native library missing: {path} (run heliox_b200/build.py)")
+    L = C.CDLL(path)
+    for name, (res, args) in SIGNATURES.items():
+        f = getattr(L, name)
+        f.restype = res
+        f.argtypes = args
+    _LIB = L
+    return L
+
+
+def dptr(x: np.ndarray):
+    return x.ctypes.data_as(_dp)
+
+
+def iptr(x: np.ndarray):
+    return x.ctypes.data_as(_ip)
+
+
+def fptr(x: np.ndarray):
+    return x.ctypes.data_as(_fp)
+
+
+class BoundGroup:
+    """A GroupDesc pointing at contiguous numpy copies of a CellGroup's arrays."""
+
+    def __init__(self, g):
+        self.keep = []
+
+        def D(x):
+            x = np.ascontiguousarray(x, dtype=np.float64)
+            self.keep.append(x)
+            return dptr(x)
+
+        def I(x):
+            x = np.ascontiguousarray(x, dtype=np.int32)
+            self.keep.append(x)
+            return iptr(x)
+
+        s = GroupDesc()
+        s.ncell, s.nnode = g.ncell, g.nnode
+        s.parent = I(g.parent)
+        s.a, s.b, s.area, s.cm = D(g.a), D(g.b), D(g.area), D(g.cm)
+        s.celsius, s.dt = float(g.celsius), float(g.dt)
+        h = g.hh
+        s.nhh = h.n
+        s.hh_node = I(h.nodes)
+        s.hh_gnabar, s.hh_gkbar, s.hh_gl, s.hh_el = (D(h.fields[k]) for k in ("gnabar", "gkbar", "gl", "el"))
+        s.hh_ena, s.hh_ek = D(h.fields["ena"]), D(h.fields["ek"])
+        p = g.pas
+        s.npas = p.n
+        s.pas_node = I(p.nodes)
+        s.pas_g, s.pas_e = D(p.fields["g"]), D(p.fields["e"])
+        c = g.iclamp
+        s.nic = c.n
+        s.ic_node = I(c.nodes)
+        s.ic_del, s.ic_dur, s.ic_amp = D(c.fields["del"]), D(c.fields["dur"]), D(c.fields["amp"])
+        self.desc = s
+
+
+def plan_check(g, nodes_per_pack: int = 0):
+    """Host-only plan build + CPU check of the planned Hines order (no GPU needed)."""
+    L = load()
+    b = BoundGroup(g)
+    st = PlanStats()
+    diff = C.c_double(-1.0)
+    rc = L.hx_plan_check(C.byref(b.desc), int(nodes_per_pack), C.byref(st), C.byref(diff))
+    if rc != 0:
+        raise ValueError(f"hx_plan_check failed (rc={rc})")
+    return st.as_dict(), float(diff.value)

@@ -1,0 +1,778 @@
+// hx_runtime.cu -- the C ABI (include/heliox_b200.h) over the plan and kernels.
+//
+// Owns device buffers (grow-only, reused across calls like the reference's
+// LearnRuntime::ensure_buf, src/runtime_api/learn/LearnRuntime.cpp:877-895),
+// the forward tape / checkpoint policy and the launch stream.  All work is
+// enqueued on one stream; host-buffer entry points stage through pinned memory.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <random>
+#include <string>
+#include <vector>
+
+#include "heliox_b200.h"
+#include "hx_dev.hpp"
+#include "hx_kernels.hpp"
+#include "hx_plan.hpp"
+
+namespace {
+
+template <typename T>
+struct DevBuf {
+    T* p = nullptr;
+    size_t n = 0;
+    ~DevBuf() { release(); }
+    void release() {
+        if (p) cudaFree(p);
+        p = nullptr;
+        n = 0;
+    }
+    cudaError_t ensure(size_t count) {
+        if (count <= n && p) return cudaSuccess;
+        release();
+        size_t c = count ? count : 1;
+        cudaError_t e = cudaMalloc((void**)&p, c * sizeof(T));
+        if (e == cudaSuccess) n = c;
+        return e;
+    }
+    cudaError_t upload(const std::vector<T>& v, cudaStream_t st) {
+        cudaError_t e = ensure(v.size());
+        if (e != cudaSuccess || v.empty()) return e;
+        return cudaMemcpyAsync(p, v.data(), v.size() * sizeof(T), cudaMemcpyHostToDevice, st);
+    }
+};
+
+struct PinBuf {
+    void* p = nullptr;
+    size_t bytes = 0;
+    ~PinBuf() {
+        if (p) cudaFreeHost(p);
+    }
+    cudaError_t ensure(size_t b) {
+        if (b <= bytes && p) return cudaSuccess;
+        if (p) cudaFreeHost(p);
+        p = nullptr;
+        bytes = 0;
+        cudaError_t e = cudaMallocHost(&p, b ? b : 16);
+        if (e == cudaSuccess) bytes = b ? b : 16;
+        return e;
+    }
+};
+
+}  // namespace
+
+struct hx_ctx {
+    int device = 0;
+    cudaStream_t own = nullptr, st = nullptr;
+    std::string err;
+    int pack_target = 0;
+    size_t tape_budget = 0;
+    bool loaded = false;
+    hx::Plan P;
+    double dt = 0.025, celsius = 6.3;
+    // plan arrays
+    DevBuf<int> pack_node_off, pack_hh_off, pack_br_off, pack_lvl_off, pack_nlev, level_br_off;
+    DevBuf<int> br_head, br_end, br_parent, br_child_off, br_child;
+    DevBuf<int> node_parent, node_child_off, node_child, node_hh, node_pas, node_ic_off, node_ic;
+    DevBuf<int> ref2gpu_node, ref2gpu_hh, ref2gpu_pas, ref2gpu_ic;
+    DevBuf<int> gpu2ref_node, gpu2ref_hh, gpu2ref_pas, gpu2ref_ic;
+    // parameters (GPU order); params[kind]
+    DevBuf<double> a, b, area;
+    DevBuf<double> prm[HX_P_COUNT];
+    DevBuf<double> hh_ena, hh_ek, ic_del, ic_dur;
+    hx::DevGroup G{};
+    // state, tape, checkpoints, adjoint, gradients
+    DevBuf<double> sv, sm, sh, sn;
+    DevBuf<double> tv, tm, th, tn;
+    DevBuf<double> ck;  // nseg x (nnode + 3 nhh)
+    DevBuf<double> lv, lm, lh, ln;
+    DevBuf<double> grad;  // concatenated per kind
+    size_t grad_off[HX_P_COUNT + 1] = {0};
+    DevBuf<double> tmid;
+    DevBuf<int> pr_off, pr_local, pr_slot;
+    std::vector<int> probe_key;
+    int nprobe = 0;
+    DevBuf<double> trace_dev, dLdv_dev, stage_dev;
+    DevBuf<int> red_off, red_flat;
+    DevBuf<float> red_scale, red_out;
+    PinBuf pin;
+    // capture bookkeeping
+    bool captured = false;
+    int nstep = 0;
+    int seg = 0, nseg = 0;  // steps per segment (checkpoint interval) and count
+    bool full_tape = true;
+    cudaEvent_t ev[4] = {nullptr, nullptr, nullptr, nullptr};
+    int launches[2] = {0, 0};
+};
+
+static int fail(hx_ctx* c, const std::string& m) {
+    if (c) c->err = m;
+    return -1;
+}
+
+#define HXC(call)                                                                                    \
+    do {                                                                                             \
+        cudaError_t _e = (call);                                                                     \
+        if (_e != cudaSuccess) return fail(ctx, std::string(#call) + ": " + cudaGetErrorString(_e)); \
+    } while (0)
+
+static size_t kind_count(const hx::Plan& P, int kind) {
+    switch (kind) {
+        case HX_P_HH_GNABAR:
+        case HX_P_HH_GKBAR:
+        case HX_P_HH_GL:
+        case HX_P_HH_EL:
+            return (size_t)P.nhh;
+        case HX_P_PAS_G:
+        case HX_P_PAS_E:
+            return (size_t)P.npas;
+        case HX_P_CM:
+            return (size_t)P.nnode;
+        case HX_P_IC_AMP:
+            return (size_t)P.nic;
+    }
+    return 0;
+}
+
+static const std::vector<int>& kind_gpu2ref(const hx::Plan& P, int kind) {
+    if (kind <= HX_P_HH_EL) return P.hh_gpu2ref;
+    if (kind <= HX_P_PAS_E) return P.pas_gpu2ref;
+    if (kind == HX_P_CM) return P.gpu2ref;
+    return P.ic_gpu2ref;
+}
+
+static int* kind_ref2gpu_dev(hx_ctx* c, int kind) {
+    if (kind <= HX_P_HH_EL) return c->ref2gpu_hh.p;
+    if (kind <= HX_P_PAS_E) return c->ref2gpu_pas.p;
+    if (kind == HX_P_CM) return c->ref2gpu_node.p;
+    return c->ref2gpu_ic.p;
+}
+
+static std::vector<int> invert(const std::vector<int>& g2r, size_t n) {
+    std::vector<int> r2g(std::max<size_t>(n, 1), 0);
+    for (size_t i = 0; i < g2r.size(); i++) r2g[g2r[i]] = (int)i;
+    return r2g;
+}
+
+extern "C" {
+
+int hx_abi_version(void) { return HX_ABI_VERSION; }
+
+int hx_create(hx_ctx** out, int device) {
+    if (!out) return -1;
+    *out = nullptr;
+    int ndev = 0;
+    if (cudaGetDeviceCount(&ndev) != cudaSuccess || ndev <= 0) return -2;
+    if (device < 0 || device >= ndev) return -3;
+    hx_ctx* ctx = new hx_ctx();
+    ctx->device = device;
+    if (cudaSetDevice(device) != cudaSuccess || cudaStreamCreateWithFlags(&ctx->own, cudaStreamNonBlocking) != cudaSuccess) {
+        delete ctx;
+        return -4;
+    }
+    ctx->st = ctx->own;
+    for (auto& e : ctx->ev) cudaEventCreate(&e);
+    *out = ctx;
+    return 0;
+}
+
+int hx_destroy(hx_ctx* ctx) {
+    if (!ctx) return 0;
+    cudaSetDevice(ctx->device);
+    cudaStreamSynchronize(ctx->st);
+    for (auto& e : ctx->ev)
+        if (e) cudaEventDestroy(e);
+    if (ctx->own) cudaStreamDestroy(ctx->own);
+    delete ctx;
+    return 0;
+}
+
+const char* hx_last_error(hx_ctx* ctx) { return ctx ? ctx->err.c_str() : "null context"; }
+
+int hx_set_stream(hx_ctx* ctx, void* stream) {
+    if (!ctx) return -1;
+    ctx->st = stream ? (cudaStream_t)stream : ctx->own;
+    return 0;
+}
+
+int hx_set_pack_target(hx_ctx* ctx, int nodes_per_pack) {
+    if (!ctx) return -1;
+    if (nodes_per_pack < 0) return fail(ctx, "nodes_per_pack must be >= 0");
+    ctx->pack_target = nodes_per_pack;
+    return 0;
+}
+
+int hx_set_tape_budget(hx_ctx* ctx, size_t bytes) {
+    if (!ctx) return -1;
+    ctx->tape_budget = bytes;
+    return 0;
+}
+
+int hx_plan_check(const hx_group_desc* desc, int nodes_per_pack, hx_plan_stats* out, double* max_abs_diff) {
+    if (!desc) return -1;
+    hx::Plan P;
+    std::string e = hx::build_plan(*desc, nodes_per_pack, P);
+    if (!e.empty()) {
+        fprintf(stderr, "hx_plan_check: %s\n", e.c_str());
+        return -2;
+    }
+    if (out) {
+        out->npack = P.npack;
+        out->max_pack_nodes = P.max_pack_nodes;
+        out->max_pack_hh = P.max_pack_hh;
+        out->max_levels = P.max_levels;
+        out->max_crit_nodes = P.max_crit;
+        out->nbranch = (int)P.br_head.size();
+        out->imbalance = P.imbalance;
+        out->smem_fwd = sizeof(double) * (5 * (size_t)P.max_pack_nodes + 3 * (size_t)P.max_pack_hh);
+        out->smem_bwd = sizeof(double) * (7 * (size_t)P.max_pack_nodes + 3 * (size_t)P.max_pack_hh);
+    }
+    if (max_abs_diff) {
+        // seeded diagonally dominant system; serial solve in reference order vs planned schedule
+        const int n = desc->nnode;
+        std::mt19937_64 rng(12345);
+        std::uniform_real_distribution<double> U(0.5, 1.5);
+        double worst = 0.0;
+        for (int transposed = 0; transposed < 2; transposed++) {
+            std::vector<double> d(n), r(n);
+            for (int i = 0; i < n; i++) {
+                d[i] = 40.0 * U(rng) + 10.0;
+                r[i] = U(rng) - 1.0;
+            }
+            for (int i = desc->ncell; i < n; i++) {
+                d[i] -= desc->b[i];
+                d[desc->parent[i]] -= desc->a[i];
+            }
+            std::vector<double> ds = d, rs = r;
+            const double* A = transposed ? desc->b : desc->a;
+            const double* Uc = transposed ? desc->a : desc->b;
+            for (int i = n - 1; i >= desc->ncell; i--) {
+                int p = desc->parent[i];
+                double f = A[i] / ds[i];
+                ds[p] -= f * Uc[i];
+                rs[p] -= f * rs[i];
+            }
+            for (int i = 0; i < desc->ncell; i++) rs[i] /= ds[i];
+            for (int i = desc->ncell; i < n; i++) {
+                rs[i] -= Uc[i] * rs[desc->parent[i]];
+                rs[i] /= ds[i];
+            }
+            std::vector<double> ag(n), bg(n), dg(n), rg(n);
+            for (int gi = 0; gi < n; gi++) {
+                int ref = P.gpu2ref[gi];
+                ag[gi] = desc->a[ref];
+                bg[gi] = desc->b[ref];
+                dg[gi] = d[ref];
+                rg[gi] = r[ref];
+            }
+            hx::planned_solve_cpu(P, ag.data(), bg.data(), dg.data(), rg.data(), transposed != 0);
+            for (int gi = 0; gi < n; gi++) worst = std::max(worst, std::fabs(rg[gi] - rs[P.gpu2ref[gi]]));
+        }
+        *max_abs_diff = worst;
+    }
+    return 0;
+}
+
+int hx_load_group(hx_ctx* ctx, const hx_group_desc* desc) {
+    if (!ctx || !desc) return fail(ctx, "null argument");
+    HXC(cudaSetDevice(ctx->device));
+    ctx->loaded = false;
+    ctx->captured = false;
+    std::string e = hx::build_plan(*desc, ctx->pack_target, ctx->P);
+    if (!e.empty()) return fail(ctx, "invalid group: " + e);
+    const hx::Plan& P = ctx->P;
+    cudaStream_t st = ctx->st;
+    ctx->dt = desc->dt;
+    ctx->celsius = desc->celsius;
+    HXC(ctx->pack_node_off.upload(P.pack_node_off, st));
+    HXC(ctx->pack_hh_off.upload(P.pack_hh_off, st));
+    HXC(ctx->pack_br_off.upload(P.pack_br_off, st));
+    HXC(ctx->pack_lvl_off.upload(P.pack_lvl_off, st));
+    HXC(ctx->pack_nlev.upload(P.pack_nlev, st));
+    HXC(ctx->level_br_off.upload(P.level_br_off, st));
+    HXC(ctx->br_head.upload(P.br_head, st));
+    HXC(ctx->br_end.upload(P.br_end, st));
+    HXC(ctx->br_parent.upload(P.br_parent, st));
+    HXC(ctx->br_child_off.upload(P.br_child_off, st));
+    HXC(ctx->br_child.upload(P.br_child, st));
+    HXC(ctx->node_parent.upload(P.node_parent, st));
+    HXC(ctx->node_child_off.upload(P.node_child_off, st));
+    HXC(ctx->node_child.upload(P.node_child, st));
+    HXC(ctx->node_hh.upload(P.node_hh, st));
+    HXC(ctx->node_pas.upload(P.node_pas, st));
+    HXC(ctx->node_ic_off.upload(P.node_ic_off, st));
+    HXC(ctx->node_ic.upload(P.node_ic, st));
+    HXC(ctx->gpu2ref_node.upload(P.gpu2ref, st));
+    HXC(ctx->ref2gpu_node.upload(P.ref2gpu, st));
+    HXC(ctx->gpu2ref_hh.upload(P.hh_gpu2ref.empty() ? std::vector<int>{0} : P.hh_gpu2ref, st));
+    HXC(ctx->gpu2ref_pas.upload(P.pas_gpu2ref.empty() ? std::vector<int>{0} : P.pas_gpu2ref, st));
+    HXC(ctx->gpu2ref_ic.upload(P.ic_gpu2ref.empty() ? std::vector<int>{0} : P.ic_gpu2ref, st));
+    HXC(ctx->ref2gpu_hh.upload(invert(P.hh_gpu2ref, P.nhh), st));
+    HXC(ctx->ref2gpu_pas.upload(invert(P.pas_gpu2ref, P.npas), st));
+    HXC(ctx->ref2gpu_ic.upload(invert(P.ic_gpu2ref, P.nic), st));
+
+    auto perm = [&](const double* src, const std::vector<int>& g2r, size_t n) {
+        std::vector<double> out(std::max<size_t>(n, 1), 0.0);
+        for (size_t i = 0; i < n; i++) out[i] = src[g2r[i]];
+        return out;
+    };
+    const size_t nn = P.nnode, nh = P.nhh, np = P.npas, nc = P.nic;
+    HXC(ctx->a.upload(perm(desc->a, P.gpu2ref, nn), st));
+    HXC(ctx->b.upload(perm(desc->b, P.gpu2ref, nn), st));
+    HXC(ctx->area.upload(perm(desc->area, P.gpu2ref, nn), st));
+    HXC(ctx->prm[HX_P_CM].upload(perm(desc->cm, P.gpu2ref, nn), st));
+    HXC(ctx->prm[HX_P_HH_GNABAR].upload(perm(desc->hh_gnabar, P.hh_gpu2ref, nh), st));
+    HXC(ctx->prm[HX_P_HH_GKBAR].upload(perm(desc->hh_gkbar, P.hh_gpu2ref, nh), st));
+    HXC(ctx->prm[HX_P_HH_GL].upload(perm(desc->hh_gl, P.hh_gpu2ref, nh), st));
+    HXC(ctx->prm[HX_P_HH_EL].upload(perm(desc->hh_el, P.hh_gpu2ref, nh), st));
+    HXC(ctx->hh_ena.upload(perm(desc->hh_ena, P.hh_gpu2ref, nh), st));
+    HXC(ctx->hh_ek.upload(perm(desc->hh_ek, P.hh_gpu2ref, nh), st));
+    HXC(ctx->prm[HX_P_PAS_G].upload(perm(desc->pas_g, P.pas_gpu2ref, np), st));
+    HXC(ctx->prm[HX_P_PAS_E].upload(perm(desc->pas_e, P.pas_gpu2ref, np), st));
+    HXC(ctx->ic_del.upload(perm(desc->ic_del, P.ic_gpu2ref, nc), st));
+    HXC(ctx->ic_dur.upload(perm(desc->ic_dur, P.ic_gpu2ref, nc), st));
+    HXC(ctx->prm[HX_P_IC_AMP].upload(perm(desc->ic_amp, P.ic_gpu2ref, nc), st));
+
+    HXC(ctx->sv.ensure(nn));
+    HXC(ctx->sm.ensure(nh));
+    HXC(ctx->sh.ensure(nh));
+    HXC(ctx->sn.ensure(nh));
+    HXC(ctx->lv.ensure(nn));
+    HXC(ctx->lm.ensure(nh));
+    HXC(ctx->lh.ensure(nh));
+    HXC(ctx->ln.ensure(nh));
+    ctx->grad_off[0] = 0;
+    for (int k = 0; k < HX_P_COUNT; k++) ctx->grad_off[k + 1] = ctx->grad_off[k] + kind_count(P, k);
+    HXC(ctx->grad.ensure(ctx->grad_off[HX_P_COUNT]));
+
+    hx::DevGroup& G = ctx->G;
+    G = hx::DevGroup{};
+    G.npack = P.npack;
+    G.nnode = P.nnode;
+    G.nhh = P.nhh;
+    G.npas = P.npas;
+    G.nic = P.nic;
+    G.smem_n = std::max(P.max_pack_nodes, 1);
+    G.smem_nh = std::max(P.max_pack_hh, 1);
+    G.pack_node_off = ctx->pack_node_off.p;
+    G.pack_hh_off = ctx->pack_hh_off.p;
+    G.pack_br_off = ctx->pack_br_off.p;
+    G.pack_lvl_off = ctx->pack_lvl_off.p;
+    G.pack_nlev = ctx->pack_nlev.p;
+    G.level_br_off = ctx->level_br_off.p;
+    G.br_head = ctx->br_head.p;
+    G.br_end = ctx->br_end.p;
+    G.br_parent = ctx->br_parent.p;
+    G.br_child_off = ctx->br_child_off.p;
+    G.br_child = ctx->br_child.p;
+    G.node_parent = ctx->node_parent.p;
+    G.node_child_off = ctx->node_child_off.p;
+    G.node_child = ctx->node_child.p;
+    G.node_hh = ctx->node_hh.p;
+    G.node_pas = ctx->node_pas.p;
+    G.node_ic_off = ctx->node_ic_off.p;
+    G.node_ic = ctx->node_ic.p;
+    G.a = ctx->a.p;
+    G.b = ctx->b.p;
+    G.cm = ctx->prm[HX_P_CM].p;
+    G.area = ctx->area.p;
+    G.hh_gnabar = ctx->prm[HX_P_HH_GNABAR].p;
+    G.hh_gkbar = ctx->prm[HX_P_HH_GKBAR].p;
+    G.hh_gl = ctx->prm[HX_P_HH_GL].p;
+    G.hh_el = ctx->prm[HX_P_HH_EL].p;
+    G.hh_ena = ctx->hh_ena.p;
+    G.hh_ek = ctx->hh_ek.p;
+    G.pas_g = ctx->prm[HX_P_PAS_G].p;
+    G.pas_e = ctx->prm[HX_P_PAS_E].p;
+    G.ic_del = ctx->ic_del.p;
+    G.ic_dur = ctx->ic_dur.p;
+    G.ic_amp = ctx->prm[HX_P_IC_AMP].p;
+    G.dt = desc->dt;
+    G.cfac = 0.001 * (1.0 / desc->dt);                   // capac.cpp:56,70 with cj = 1/dt
+    G.q10 = std::pow(3.0, (desc->celsius - 6.3) / 10);   // hh_templated.cu:90
+    size_t sf = hx::fwd_smem_bytes(G), sb = hx::bwd_smem_bytes(G);
+    int maxsmem = 0;
+    HXC(cudaDeviceGetAttribute(&maxsmem, cudaDevAttrMaxSharedMemoryPerBlockOptin, ctx->device));
+    if (sb > (size_t)maxsmem || sf > (size_t)maxsmem)
+        return fail(ctx, "cell pack needs " + std::to_string(sb) + " B shared memory (> " + std::to_string(maxsmem) +
+                             "); lower the pack target or split the cell");
+    HXC(hx::configure_kernels(sf, sb));
+    HXC(cudaStreamSynchronize(st));
+    ctx->loaded = true;
+    return 0;
+}
+
+int hx_get_plan_stats(hx_ctx* ctx, hx_plan_stats* out) {
+    if (!ctx || !out) return -1;
+    if (!ctx->loaded) return fail(ctx, "no group loaded");
+    const hx::Plan& P = ctx->P;
+    out->npack = P.npack;
+    out->max_pack_nodes = P.max_pack_nodes;
+    out->max_pack_hh = P.max_pack_hh;
+    out->max_levels = P.max_levels;
+    out->max_crit_nodes = P.max_crit;
+    out->nbranch = (int)P.br_head.size();
+    out->imbalance = P.imbalance;
+    out->smem_fwd = hx::fwd_smem_bytes(ctx->G);
+    out->smem_bwd = hx::bwd_smem_bytes(ctx->G);
+    return 0;
+}
+
+int hx_set_param(hx_ctx* ctx, int kind, const double* values, int n) {
+    if (!ctx || !values) return fail(ctx, "null argument");
+    if (!ctx->loaded) return fail(ctx, "no group loaded");
+    if (kind < 0 || kind >= HX_P_COUNT) return fail(ctx, "bad parameter kind");
+    size_t cnt = kind_count(ctx->P, kind);
+    if ((size_t)n != cnt) return fail(ctx, "parameter count mismatch");
+    if (!cnt) return 0;
+    HXC(cudaSetDevice(ctx->device));
+    HXC(ctx->pin.ensure(cnt * sizeof(double)));
+    double* h = (double*)ctx->pin.p;
+    const std::vector<int>& g2r = kind_gpu2ref(ctx->P, kind);
+    HXC(cudaStreamSynchronize(ctx->st));  // pinned staging buffer may still be in use
+    for (size_t i = 0; i < cnt; i++) h[i] = values[g2r[i]];
+    HXC(cudaMemcpyAsync(ctx->prm[kind].p, h, cnt * sizeof(double), cudaMemcpyHostToDevice, ctx->st));
+    HXC(cudaStreamSynchronize(ctx->st));
+    return 0;
+}
+
+int hx_get_param(hx_ctx* ctx, int kind, double* values, int n) {
+    if (!ctx || !values) return fail(ctx, "null argument");
+    if (!ctx->loaded) return fail(ctx, "no group loaded");
+    if (kind < 0 || kind >= HX_P_COUNT) return fail(ctx, "bad parameter kind");
+    size_t cnt = kind_count(ctx->P, kind);
+    if ((size_t)n != cnt) return fail(ctx, "parameter count mismatch");
+    if (!cnt) return 0;
+    HXC(cudaSetDevice(ctx->device));
+    HXC(ctx->stage_dev.ensure(cnt));
+    HXC(hx::launch_gather(ctx->prm[kind].p, kind_ref2gpu_dev(ctx, kind), ctx->stage_dev.p, (int)cnt, ctx->st));
+    HXC(cudaMemcpyAsync(values, ctx->stage_dev.p, cnt * sizeof(double), cudaMemcpyDeviceToHost, ctx->st));
+    HXC(cudaStreamSynchronize(ctx->st));
+    return 0;
+}
+
+}  // extern "C"
+
+// ---------------------------------------------------------------- capture / backward internals
+static int setup_probes(hx_ctx* ctx, int nprobe, const int* probe_nodes) {
+    if (nprobe < 0 || (nprobe > 0 && !probe_nodes)) return fail(ctx, "bad probe list");
+    const hx::Plan& P = ctx->P;
+    std::vector<int> key(probe_nodes, probe_nodes + nprobe);
+    if (key == ctx->probe_key && ctx->pr_off.p) return 0;
+    std::vector<std::vector<std::pair<int, int>>> per(P.npack);
+    for (int q = 0; q < nprobe; q++) {
+        int r = probe_nodes[q];
+        if (r < 0 || r >= P.nnode) return fail(ctx, "probe node out of range");
+        int gi = P.ref2gpu[r];
+        int pk = (int)(std::upper_bound(P.pack_node_off.begin(), P.pack_node_off.end(), gi) - P.pack_node_off.begin()) - 1;
+        per[pk].push_back({gi - P.pack_node_off[pk], q});
+    }
+    std::vector<int> off(P.npack + 1, 0), loc, slot;
+    for (int p = 0; p < P.npack; p++) {
+        for (auto& pr : per[p]) {
+            loc.push_back(pr.first);
+            slot.push_back(pr.second);
+        }
+        off[p + 1] = (int)loc.size();
+    }
+    if (loc.empty()) {
+        loc.push_back(0);
+        slot.push_back(0);
+    }
+    HXC(ctx->pr_off.upload(off, ctx->st));
+    HXC(ctx->pr_local.upload(loc, ctx->st));
+    HXC(ctx->pr_slot.upload(slot, ctx->st));
+    ctx->probe_key = key;
+    ctx->nprobe = nprobe;
+    return 0;
+}
+
+static hx::DevProbe probe_view(hx_ctx* c) {
+    hx::DevProbe p;
+    p.pack_off = c->pr_off.p;
+    p.local = c->pr_local.p;
+    p.slot = c->pr_slot.p;
+    p.nprobe = c->nprobe;
+    return p;
+}
+
+static int setup_time(hx_ctx* ctx, int nstep) {
+    // t accumulates in half steps exactly as Simulate::fadvance_cpu does
+    // (simulate.cpp:417 and :774); IClamp sees the mid-step value.
+    std::vector<double> tm(std::max(nstep, 1));
+    double t = 0.0;
+    for (int k = 0; k < nstep; k++) {
+        t += 0.5 * ctx->dt;
+        tm[k] = t;
+        t += 0.5 * ctx->dt;
+    }
+    HXC(ctx->tmid.upload(tm, ctx->st));
+    return 0;
+}
+
+static int plan_tape(hx_ctx* ctx, int nstep) {
+    const size_t nn = ctx->P.nnode, nh = ctx->P.nhh;
+    const size_t per_step = (nn + 3 * nh) * sizeof(double);
+    size_t budget = ctx->tape_budget;
+    if (!budget) {
+        size_t fr = 0, tot = 0;
+        HXC(cudaMemGetInfo(&fr, &tot));
+        budget = (size_t)(0.6 * (double)(fr + ctx->tv.n * sizeof(double) + 3 * ctx->tm.n * sizeof(double)));
+    }
+    const size_t full = per_step * (size_t)(nstep + 1);
+    if (full <= budget) {
+        ctx->full_tape = true;
+        ctx->seg = nstep;
+        ctx->nseg = 1;
+        HXC(ctx->tv.ensure(nn * (size_t)(nstep + 1)));
+        HXC(ctx->tm.ensure(nh * (size_t)nstep + 1));
+        HXC(ctx->th.ensure(nh * (size_t)nstep + 1));
+        HXC(ctx->tn.ensure(nh * (size_t)nstep + 1));
+        return 0;
+    }
+    // checkpointed: segments of K steps; K*per_step (segment tape) + nseg*per_step (checkpoints) <= budget
+    size_t K = (size_t)std::sqrt((double)nstep);
+    if (K < 1) K = 1;
+    while (K > 1 && (K + 1 + ((size_t)nstep + K - 1) / K) * per_step > budget) K /= 2;
+    if ((K + 1 + ((size_t)nstep + K - 1) / K) * per_step > budget)
+        return fail(ctx, "device memory too small for even a one-step tape");
+    ctx->full_tape = false;
+    ctx->seg = (int)K;
+    ctx->nseg = (int)(((size_t)nstep + K - 1) / K);
+    HXC(ctx->tv.ensure(nn * (K + 1)));
+    HXC(ctx->tm.ensure(nh * K + 1));
+    HXC(ctx->th.ensure(nh * K + 1));
+    HXC(ctx->tn.ensure(nh * K + 1));
+    HXC(ctx->ck.ensure((nn + 3 * nh) * (size_t)ctx->nseg));
+    return 0;
+}
+
+static hx::DevState state_view(hx_ctx* c) { return hx::DevState{c->sv.p, c->sm.p, c->sh.p, c->sn.p}; }
+
+static int save_ck(hx_ctx* ctx, int s) {
+    const size_t nn = ctx->P.nnode, nh = ctx->P.nhh;
+    double* base = ctx->ck.p + (nn + 3 * nh) * (size_t)s;
+    HXC(cudaMemcpyAsync(base, ctx->sv.p, nn * 8, cudaMemcpyDeviceToDevice, ctx->st));
+    if (nh) {
+        HXC(cudaMemcpyAsync(base + nn, ctx->sm.p, nh * 8, cudaMemcpyDeviceToDevice, ctx->st));
+        HXC(cudaMemcpyAsync(base + nn + nh, ctx->sh.p, nh * 8, cudaMemcpyDeviceToDevice, ctx->st));
+        HXC(cudaMemcpyAsync(base + nn + 2 * nh, ctx->sn.p, nh * 8, cudaMemcpyDeviceToDevice, ctx->st));
+    }
+    return 0;
+}
+
+static int load_ck(hx_ctx* ctx, int s) {
+    const size_t nn = ctx->P.nnode, nh = ctx->P.nhh;
+    const double* base = ctx->ck.p + (nn + 3 * nh) * (size_t)s;
+    HXC(cudaMemcpyAsync(ctx->sv.p, base, nn * 8, cudaMemcpyDeviceToDevice, ctx->st));
+    if (nh) {
+        HXC(cudaMemcpyAsync(ctx->sm.p, base + nn, nh * 8, cudaMemcpyDeviceToDevice, ctx->st));
+        HXC(cudaMemcpyAsync(ctx->sh.p, base + nn + nh, nh * 8, cudaMemcpyDeviceToDevice, ctx->st));
+        HXC(cudaMemcpyAsync(ctx->sn.p, base + nn + 2 * nh, nh * 8, cudaMemcpyDeviceToDevice, ctx->st));
+    }
+    return 0;
+}
+
+static int run_forward(hx_ctx* ctx, int nstep, double v_init, int nprobe, const int* probe, double* trace_dev,
+                       bool capture) {
+    if (!ctx->loaded) return fail(ctx, "no group loaded");
+    if (nstep < 0) return fail(ctx, "nstep must be >= 0");
+    HXC(cudaSetDevice(ctx->device));
+    if (setup_probes(ctx, nprobe, probe)) return -1;
+    if (setup_time(ctx, nstep)) return -1;
+    hx::DevTape T{nullptr, nullptr, nullptr, nullptr, 0};
+    if (capture) {
+        if (plan_tape(ctx, nstep)) return -1;
+        T = hx::DevTape{ctx->tv.p, ctx->tm.p, ctx->th.p, ctx->tn.p, 0};
+    }
+    hx::DevState S = state_view(ctx);
+    hx::DevProbe PV = probe_view(ctx);
+    HXC(hx::launch_init(ctx->G, S, v_init, ctx->st));
+    HXC(cudaEventRecord(ctx->ev[0], ctx->st));
+    int launches = 0;
+    if (!capture || ctx->full_tape) {
+        HXC(hx::launch_fwd(ctx->G, S, T, capture ? 1 : 0, PV, trace_dev, ctx->tmid.p, 0, nstep, ctx->st));
+        launches = 1;
+    } else {
+        for (int s = 0; s < ctx->nseg; s++) {
+            if (save_ck(ctx, s)) return -1;
+            int k0 = s * ctx->seg, k1 = std::min(nstep, k0 + ctx->seg);
+            HXC(hx::launch_fwd(ctx->G, S, T, 0, PV, trace_dev, ctx->tmid.p, k0, k1, ctx->st));
+            launches++;
+        }
+    }
+    HXC(cudaEventRecord(ctx->ev[1], ctx->st));
+    ctx->launches[0] = launches;
+    ctx->captured = capture;
+    ctx->nstep = nstep;
+    return 0;
+}
+
+static int run_backward(hx_ctx* ctx, const double* dLdv_dev) {
+    if (!ctx->loaded) return fail(ctx, "no group loaded");
+    if (!ctx->captured) return fail(ctx, "hx_backward needs a preceding hx_forward_capture");
+    HXC(cudaSetDevice(ctx->device));
+    const size_t nn = ctx->P.nnode, nh = ctx->P.nhh;
+    HXC(cudaMemsetAsync(ctx->lv.p, 0, nn * 8, ctx->st));
+    if (nh) {
+        HXC(cudaMemsetAsync(ctx->lm.p, 0, nh * 8, ctx->st));
+        HXC(cudaMemsetAsync(ctx->lh.p, 0, nh * 8, ctx->st));
+        HXC(cudaMemsetAsync(ctx->ln.p, 0, nh * 8, ctx->st));
+    }
+    HXC(cudaMemsetAsync(ctx->grad.p, 0, ctx->grad_off[HX_P_COUNT] * 8, ctx->st));
+    hx::DevAdj A{ctx->lv.p, ctx->lm.p, ctx->lh.p, ctx->ln.p};
+    double* g = ctx->grad.p;
+    hx::DevGrad GR{g + ctx->grad_off[HX_P_HH_GNABAR], g + ctx->grad_off[HX_P_HH_GKBAR], g + ctx->grad_off[HX_P_HH_GL],
+                   g + ctx->grad_off[HX_P_HH_EL],     g + ctx->grad_off[HX_P_PAS_G],   g + ctx->grad_off[HX_P_PAS_E],
+                   g + ctx->grad_off[HX_P_CM],        g + ctx->grad_off[HX_P_IC_AMP]};
+    hx::DevProbe PV = probe_view(ctx);
+    hx::DevState S = state_view(ctx);
+    HXC(cudaEventRecord(ctx->ev[2], ctx->st));
+    int launches = 0;
+    if (ctx->full_tape) {
+        hx::DevTape T{ctx->tv.p, ctx->tm.p, ctx->th.p, ctx->tn.p, 0};
+        HXC(hx::launch_bwd(ctx->G, T, A, GR, PV, dLdv_dev, ctx->tmid.p, ctx->nstep, 0, ctx->st));
+        launches = 1;
+    } else {
+        for (int s = ctx->nseg - 1; s >= 0; s--) {
+            int k0 = s * ctx->seg, k1 = std::min(ctx->nstep, k0 + ctx->seg);
+            if (load_ck(ctx, s)) return -1;
+            hx::DevTape T{ctx->tv.p, ctx->tm.p, ctx->th.p, ctx->tn.p, k0};
+            HXC(hx::launch_fwd(ctx->G, S, T, 1, PV, nullptr, ctx->tmid.p, k0, k1, ctx->st));
+            HXC(hx::launch_bwd(ctx->G, T, A, GR, PV, dLdv_dev, ctx->tmid.p, k1, k0, ctx->st));
+            launches += 2;
+        }
+    }
+    HXC(cudaEventRecord(ctx->ev[3], ctx->st));
+    ctx->launches[1] = launches;
+    return 0;
+}
+
+static int gather_grads_dev(hx_ctx* ctx, double* const* grads_dev) {
+    if (!grads_dev) return 0;
+    for (int k = 0; k < HX_P_COUNT; k++) {
+        if (!grads_dev[k]) continue;
+        size_t cnt = kind_count(ctx->P, k);
+        HXC(hx::launch_gather(ctx->grad.p + ctx->grad_off[k], kind_ref2gpu_dev(ctx, k), grads_dev[k], (int)cnt, ctx->st));
+    }
+    return 0;
+}
+
+extern "C" {
+
+int hx_simulate(hx_ctx* ctx, int nstep, double v_init, int nprobe, const int* probe_nodes, double* trace) {
+    if (!ctx) return -1;
+    size_t tn = (size_t)(nstep + 1) * (size_t)nprobe;
+    HXC(ctx->trace_dev.ensure(tn));
+    if (run_forward(ctx, nstep, v_init, nprobe, probe_nodes, ctx->trace_dev.p, false)) return -1;
+    if (trace && tn) HXC(cudaMemcpyAsync(trace, ctx->trace_dev.p, tn * 8, cudaMemcpyDeviceToHost, ctx->st));
+    HXC(cudaStreamSynchronize(ctx->st));
+    return 0;
+}
+
+int hx_forward_capture(hx_ctx* ctx, int nstep, double v_init, int nprobe, const int* probe_nodes, double* trace) {
+    if (!ctx) return -1;
+    size_t tn = (size_t)(nstep + 1) * (size_t)nprobe;
+    HXC(ctx->trace_dev.ensure(tn));
+    if (run_forward(ctx, nstep, v_init, nprobe, probe_nodes, ctx->trace_dev.p, true)) return -1;
+    if (trace && tn) HXC(cudaMemcpyAsync(trace, ctx->trace_dev.p, tn * 8, cudaMemcpyDeviceToHost, ctx->st));
+    HXC(cudaStreamSynchronize(ctx->st));
+    return 0;
+}
+
+int hx_forward_capture_dev(hx_ctx* ctx, int nstep, double v_init, int nprobe, const int* probe_nodes,
+                           double* trace_dev) {
+    if (!ctx) return -1;
+    return run_forward(ctx, nstep, v_init, nprobe, probe_nodes, trace_dev, true);
+}
+
+int hx_backward(hx_ctx* ctx, const double* dLdv, double* const* grads) {
+    if (!ctx || !dLdv) return fail(ctx, "null argument");
+    if (!ctx->captured) return fail(ctx, "hx_backward needs a preceding hx_forward_capture");
+    size_t tn = (size_t)(ctx->nstep + 1) * (size_t)ctx->nprobe;
+    HXC(ctx->dLdv_dev.ensure(tn));
+    if (tn) HXC(cudaMemcpyAsync(ctx->dLdv_dev.p, dLdv, tn * 8, cudaMemcpyHostToDevice, ctx->st));
+    if (run_backward(ctx, ctx->dLdv_dev.p)) return -1;
+    if (grads) {
+        HXC(ctx->stage_dev.ensure(ctx->grad_off[HX_P_COUNT]));
+        for (int k = 0; k < HX_P_COUNT; k++) {
+            if (!grads[k]) continue;
+            size_t cnt = kind_count(ctx->P, k);
+            if (!cnt) continue;
+            double* sd = ctx->stage_dev.p + ctx->grad_off[k];
+            HXC(hx::launch_gather(ctx->grad.p + ctx->grad_off[k], kind_ref2gpu_dev(ctx, k), sd, (int)cnt, ctx->st));
+            HXC(cudaMemcpyAsync(grads[k], sd, cnt * 8, cudaMemcpyDeviceToHost, ctx->st));
+        }
+    }
+    HXC(cudaStreamSynchronize(ctx->st));
+    return 0;
+}
+
+int hx_backward_dev(hx_ctx* ctx, const double* dLdv_dev, double* const* grads_dev) {
+    if (!ctx || !dLdv_dev) return fail(ctx, "null argument");
+    if (run_backward(ctx, dLdv_dev)) return -1;
+    return gather_grads_dev(ctx, grads_dev);
+}
+
+int hx_reduce_grads_f32(hx_ctx* ctx, int n, const int* kind, const int* index, const int32_t* dest,
+                        const float* scale, float* out, int n_out) {
+    if (!ctx || n < 0 || n_out < 0 || (n && (!kind || !index || !dest || !scale)) || (n_out && !out))
+        return fail(ctx, "bad argument");
+    if (!ctx->captured) return fail(ctx, "hx_reduce_grads_f32 needs a preceding backward");
+    HXC(cudaSetDevice(ctx->device));
+    std::vector<int> cnt(n_out + 1, 0);
+    for (int e = 0; e < n; e++) {
+        if (dest[e] < 0 || dest[e] >= n_out) return fail(ctx, "dest out of range");
+        if (kind[e] < 0 || kind[e] >= HX_P_COUNT) return fail(ctx, "bad kind");
+        if (index[e] < 0 || (size_t)index[e] >= kind_count(ctx->P, kind[e])) return fail(ctx, "index out of range");
+        cnt[dest[e] + 1]++;
+    }
+    for (int c = 0; c < n_out; c++) cnt[c + 1] += cnt[c];
+    // entries grouped by destination column, stable in input order; each entry
+    // points at (offset of its kind) + (GPU index of its reference instance)
+    std::vector<int> flat(std::max(n, 1)), fill(cnt.begin(), cnt.end() - 1);
+    std::vector<float> sc(std::max(n, 1));
+    const std::vector<int> inv_hh = invert(ctx->P.hh_gpu2ref, ctx->P.nhh);
+    const std::vector<int> inv_pas = invert(ctx->P.pas_gpu2ref, ctx->P.npas);
+    const std::vector<int> inv_ic = invert(ctx->P.ic_gpu2ref, ctx->P.nic);
+    for (int e = 0; e < n; e++) {
+        const int pos = fill[dest[e]]++;
+        const int k = kind[e], r = index[e];
+        int gi;
+        if (k <= HX_P_HH_EL)
+            gi = inv_hh[r];
+        else if (k <= HX_P_PAS_E)
+            gi = inv_pas[r];
+        else if (k == HX_P_CM)
+            gi = ctx->P.ref2gpu[r];
+        else
+            gi = inv_ic[r];
+        flat[pos] = (int)ctx->grad_off[k] + gi;
+        sc[pos] = scale[e];
+    }
+    HXC(ctx->red_off.upload(cnt, ctx->st));
+    HXC(ctx->red_flat.upload(flat, ctx->st));
+    HXC(ctx->red_scale.upload(sc, ctx->st));
+    HXC(ctx->red_out.ensure(n_out));
+    HXC(hx::launch_reduce_cols(ctx->grad.p, ctx->red_off.p, ctx->red_flat.p, ctx->red_scale.p, ctx->red_out.p, n_out,
+                               ctx->st));
+    if (n_out) HXC(cudaMemcpyAsync(out, ctx->red_out.p, (size_t)n_out * 4, cudaMemcpyDeviceToHost, ctx->st));
+    HXC(cudaStreamSynchronize(ctx->st));
+    return 0;
+}
+
+int hx_last_kernel_ms(hx_ctx* ctx, int which, double* ms, int* launches) {
+    if (!ctx || (which != 0 && which != 1)) return -1;
+    HXC(cudaEventSynchronize(ctx->ev[which * 2 + 1]));
+    float f = 0.f;
+    HXC(cudaEventElapsedTime(&f, ctx->ev[which * 2], ctx->ev[which * 2 + 1]));
+    if (ms) *ms = f;
+    if (launches) *launches = ctx->launches[which];
+    return 0;
+}
+
+}  // extern "C"

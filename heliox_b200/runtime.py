@@ -1,0 +1,209 @@
+"""Host-side mirror of the reference's ``Sim`` operator surface for the hot path.
+
+The reference exposes a nanobind class ``Sim`` (src/python_api/PyBindings.cpp:12-266)
+whose learning entry points run a forward capture and a gradient replay through
+``LearnRuntime`` (src/runtime_api/learn/LearnRuntime.h:21-293).  ``Sim`` here keeps
+the same verbs -- variable handles, simulate, capture, backward, the
+MappedSignal column reduction and the external-gradient Adam optimizer -- and
+calls the native library (include/heliox_b200.h) for every computation.
+"""
+from __future__ import annotations
+
+import ctypes as C
+from typing import Dict, Iterable, Optional, Sequence
+
+import numpy as np
+
+from . import _lib
+from .model import CellGroup
+
+_MECH_VAR = {
+    ("hh", "gnabar"): "hh.gnabar",
+    ("hh", "gkbar"): "hh.gkbar",
+    ("hh", "gl"): "hh.gl",
+    ("hh", "el"): "hh.el",
+    ("pas", "g_pas"): "pas.g",
+    ("pas", "g"): "pas.g",
+    ("pas", "e_pas"): "pas.e",
+    ("pas", "e"): "pas.e",
+    ("capacitance", "cm"): "cm",
+    ("IClamp", "amp"): "IClamp.amp",
+}
+_HANDLE_SHIFT = 24
+
+
+def make_handle(key: str, index: int) -> int:
+    return (_lib.HX_P[key] << _HANDLE_SHIFT) | int(index)
+
+
+def split_handle(h: int):
+    return int(h) >> _HANDLE_SHIFT, int(h) & ((1 << _HANDLE_SHIFT) - 1)
+
+
+class HxError(RuntimeError):
+    pass
+
+
+class Sim:
+    """One simulation/learning runtime bound to one CUDA device."""
+
+    def __init__(self, device: int = 0, pack_target: int = 0, tape_budget_bytes: int = 0):
+        self._L = _lib.load()
+        ctx = C.c_void_p()
+        rc = self._L.hx_create(C.byref(ctx), int(device))
+        if rc != 0:
+            raise HxError(f"hx_create failed (rc={rc}): no usable CUDA device {device}")
+        self._ctx = ctx
+        self.device = int(device)
+        self._check(self._L.hx_set_pack_target(ctx, int(pack_target)), "hx_set_pack_target")
+        self._check(self._L.hx_set_tape_budget(ctx, int(tape_budget_bytes)), "hx_set_tape_budget")
+        self.group: Optional[CellGroup] = None
+        self._bound = None
+        self._nstep = None
+        self._probes = None
+        self._optimizers: Dict[int, "_AdamOpt"] = {}
+
+    # ------------------------------------------------------------------ basics
+    def _check(self, rc: int, what: str):
+        if rc != 0:
+            msg = self._L.hx_last_error(self._ctx)
+            raise HxError(f"{what} failed (rc={rc}): {msg.decode() if msg else ''}")
+
+    def close(self):
+        if getattr(self, "_ctx", None):
+            self._L.hx_destroy(self._ctx)
+            self._ctx = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def set_stream(self, stream_handle: int):
+        """Launch on an existing CUDA stream (e.g. ``torch.cuda.current_stream().cuda_stream``)."""
+        self._check(self._L.hx_set_stream(self._ctx, C.c_void_p(int(stream_handle))), "hx_set_stream")
+
+    def load_group(self, group: CellGroup):
+        group.validate()
+        self.group = group
+        self._bound = _lib.BoundGroup(group)
+        self._check(self._L.hx_load_group(self._ctx, C.byref(self._bound.desc)), "hx_load_group")
+
+    def plan_stats(self) -> dict:
+        st = _lib.PlanStats()
+        self._check(self._L.hx_get_plan_stats(self._ctx, C.byref(st)), "hx_get_plan_stats")
+        return st.as_dict()
+
+    # ------------------------------------------------------------------ handles / parameters
+    def get_variable_handle(self, mech: str, var: str, idx: int) -> int:
+        """Handle of one parameter instance (mirrors Sim.get_variable_handle)."""
+        key = _MECH_VAR.get((mech, var))
+        if key is None:
+            raise KeyError(f"{mech}.{var} is not a parameter of the adjoint path")
+        n = self._count(key)
+        if not 0 <= idx < n:
+            raise IndexError(f"{mech}.{var}[{idx}] out of range (n={n})")
+        return make_handle(key, idx)
+
+    def _count(self, key: str) -> int:
+        g = self.group
+        if key.startswith("hh."):
+            return g.hh.n
+        if key.startswith("pas."):
+            return g.pas.n
+        if key == "cm":
+            return g.nnode
+        return g.iclamp.n
+
+    def set_param_array(self, key: str, values: np.ndarray):
+        v = np.ascontiguousarray(values, dtype=np.float64)
+        self._check(self._L.hx_set_param(self._ctx, _lib.HX_P[key], _lib.dptr(v), int(v.shape[0])), "hx_set_param")
+
+    def get_param_array(self, key: str) -> np.ndarray:
+        out = np.zeros(self._count(key))
+        self._check(self._L.hx_get_param(self._ctx, _lib.HX_P[key], _lib.dptr(out), int(out.shape[0])), "hx_get_param")
+        return out
+
+    def set_variables(self, handles: Sequence[int], values: Sequence[float]):
+        by_kind: Dict[int, list] = {}
+        for h, v in zip(handles, values):
+            k, i = split_handle(h)
+            by_kind.setdefault(k, []).append((i, float(v)))
+        inv = {v: k for k, v in _lib.HX_P.items()}
+        for k, items in by_kind.items():
+            key = inv[k]
+            arr = self.get_param_array(key)
+            for i, v in items:
+                arr[i] = v
+            self.set_param_array(key, arr)
+
+    def get_variables(self, handles: Sequence[int]) -> np.ndarray:
+        inv = {v: k for k, v in _lib.HX_P.items()}
+        cache: Dict[int, np.ndarray] = {}
+        out = np.zeros(len(handles))
+        for j, h in enumerate(handles):
+            k, i = split_handle(h)
+            if k not in cache:
+                cache[k] = self.get_param_array(inv[k])
+            out[j] = cache[k][i]
+        return out
+
+    # ------------------------------------------------------------------ forward
+    def _probe_arr(self, probes) -> np.ndarray:
+        if probes is None:
+            probes = self.group.soma_nodes()
+        return np.ascontiguousarray(probes, dtype=np.int32)
+
+    def simulate(self, nstep: int, v_init: Optional[float] = None, probes=None) -> np.ndarray:
+        """finitialize + nstep steps; returns v at the probes, shape (nstep+1, nprobe)."""
+        p = self._probe_arr(probes)
+        tr = np.zeros((nstep + 1, p.shape[0]))
+        vi = self.group.v_init if v_init is None else v_init
+        self._check(self._L.hx_simulate(self._ctx, int(nstep), float(vi), int(p.shape[0]), _lib.iptr(p), _lib.dptr(tr)),
+                    "hx_simulate")
+        return tr
+
+    def forward_capture(self, nstep: int, v_init: Optional[float] = None, probes=None) -> np.ndarray:
+        """Forward that records the tape for ``backward``; returns the probe trace."""
+        p = self._probe_arr(probes)
+        tr = np.zeros((nstep + 1, p.shape[0]))
+        vi = self.group.v_init if v_init is None else v_init
+        self._check(
+            self._L.hx_forward_capture(self._ctx, int(nstep), float(vi), int(p.shape[0]), _lib.iptr(p), _lib.dptr(tr)),
+            "hx_forward_capture")
+        self._nstep, self._probes = int(nstep), p
+        return tr
+
+    # ------------------------------------------------------------------ backward
+    def backward(self, dLdv: np.ndarray, keys: Iterable[str] = tuple(_lib.HX_P)) -> Dict[str, np.ndarray]:
+        """Exact adjoint of the last capture; dLdv shape (nstep+1, nprobe)."""
+        if self._nstep is None:
+            raise HxError("backward needs a preceding forward_capture")
+        d = np.ascontiguousarray(dLdv, dtype=np.float64)
+        if d.shape != (self._nstep + 1, self._probes.shape[0]):
+            raise ValueError(f"dLdv must have shape {(self._nstep + 1, self._probes.shape[0])}")
+        outs = {k: np.zeros(self._count(k)) for k in keys}
+        arr = (_lib._dp * _lib.HX_P_COUNT)()
+        for k, v in outs.items():
+            arr[_lib.HX_P[k]] = _lib.dptr(v)
+        self._check(self._L.hx_backward(self._ctx, _lib.dptr(d), arr), "hx_backward")
+        return outs
+
+    def reduce_grads_f32(self, handles: Sequence[int], dest: np.ndarray, scale: np.ndarray, n_out: int) -> np.ndarray:
+        """MappedSignal column reduction of the last backward: out[dest[j]] += scale[j]*grad[handle j]."""
+        hk = np.array([split_handle(h)[0] for h in handles], dtype=np.int32)
+        hi = np.array([split_handle(h)[1] for h in handles], dtype=np.int32)
+        dest = np.ascontiguousarray(dest, dtype=np.int32)
+        scale = np.ascontiguousarray(scale, dtype=np.float32)
+        out = np.zeros(int(n_out), dtype=np.float32)
+        self._check(
+            self._L.hx_reduce_grads_f32(self._ctx, int(hk.shape[0]), _lib.iptr(hk), _lib.iptr(hi), _lib.iptr(dest),
+                                        _lib.fptr(scale), _lib.fptr(out), int(n_out)), "hx_reduce_grads_f32")
+        return out
+
+    def last_kernel_ms(self, which: int):
+        ms = C.c_double()
+        n = C.c_int()
+        self._check(self._L.hx_last_kernel_ms(self._ctx, int(which), C.byref(ms), C.byref(n)), "hx_last_kernel_ms")
+        return float(ms.value), int(n.value)

@@ -1,0 +1,146 @@
+/*
+ * heliox_b200.h -- C ABI of the B200-native forward + exact-adjoint library
+ * (heliox_b200/libhx_b200.so).
+ *
+ * Plain C: opaque context, POD arguments, int status codes (0 ok, <0 error,
+ * reason in hx_last_error), caller-owned output buffers ("_into" convention of
+ * the reference's LearnRuntime, src/runtime_api/learn/LearnRuntime.h:21-293).
+ * Pointers are HOST pointers unless the function name ends in "_dev", in which
+ * case they are device pointers on the context's device.
+ *
+ * Which reference interface each entry replaces is given beside it.
+ */
+#ifndef HELIOX_B200_H
+#define HELIOX_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define HX_ABI_VERSION 1
+
+typedef struct hx_ctx hx_ctx;
+
+/* One cell group in reference node order: first ncell nodes are roots
+ * (parent -1), parent[i] < i otherwise.  Mirrors the arrays HelioXroupData
+ * holds after data_format_trans (src/neuron.h:19-130,
+ * src/io/coredat_to_innerdat.cpp:569-603).  Mechanism instance tables are
+ * sorted by node like the reference's nodeindices. */
+typedef struct hx_group_desc {
+    int ncell, nnode;
+    const int* parent;
+    const double *a, *b, *area, *cm;
+    double celsius, dt;
+    /* hh (src/mech/user-mech/hh_templated.cu) */
+    int nhh;
+    const int* hh_node;
+    const double *hh_gnabar, *hh_gkbar, *hh_gl, *hh_el, *hh_ena, *hh_ek;
+    /* pas (src/mech/user-mech/pas_templated.cu) */
+    int npas;
+    const int* pas_node;
+    const double *pas_g, *pas_e;
+    /* IClamp (src/mech/user-mech/iclamp_templated.cu) */
+    int nic;
+    const int* ic_node;
+    const double *ic_del, *ic_dur, *ic_amp;
+} hx_group_desc;
+
+/* Parameter / gradient kinds (per mechanism instance; HX_P_CM per node). */
+enum hx_param_kind {
+    HX_P_HH_GNABAR = 0,
+    HX_P_HH_GKBAR = 1,
+    HX_P_HH_GL = 2,
+    HX_P_HH_EL = 3,
+    HX_P_PAS_G = 4,
+    HX_P_PAS_E = 5,
+    HX_P_CM = 6,
+    HX_P_IC_AMP = 7,
+    HX_P_COUNT = 8
+};
+
+/* Statistics of the execution plan built at load time. */
+typedef struct hx_plan_stats {
+    int npack;            /* CTAs (cell packs) */
+    int max_pack_nodes;   /* largest pack */
+    int max_pack_hh;
+    int max_levels;       /* branch levels of the deepest pack */
+    int max_crit_nodes;   /* longest root->leaf chain (nodes) of any pack */
+    int nbranch;          /* branches over all packs */
+    double imbalance;     /* max pack nodes / mean pack nodes */
+    size_t smem_fwd, smem_bwd; /* dynamic shared memory per CTA (bytes) */
+} hx_plan_stats;
+
+/* ---- context ------------------------------------------------------------ */
+/* Replaces SimRuntimeCore construction + Simulate(mode=GPU)
+ * (src/runtime_api/core/SimRuntimeCore.h:24-219, src/simulate.h:17-80). */
+int hx_create(hx_ctx** out, int device);
+int hx_destroy(hx_ctx* ctx);
+const char* hx_last_error(hx_ctx* ctx);
+int hx_abi_version(void);
+/* Launch on this CUDA stream (cudaStream_t passed as void*); NULL = the context's own stream. */
+int hx_set_stream(hx_ctx* ctx, void* stream);
+/* Target nodes per cell pack (CTA); 0 = default.  Must be called before hx_load_group. */
+int hx_set_pack_target(hx_ctx* ctx, int nodes_per_pack);
+/* Upper bound on device bytes the forward tape may use; when the full tape
+ * does not fit, the backward recomputes checkpointed segments.  0 = default
+ * (60% of free device memory at load time). */
+int hx_set_tape_budget(hx_ctx* ctx, size_t bytes);
+
+/* ---- model ---------------------------------------------------------------- */
+/* Replaces SimRuntimeCore::load_model -> read_coredat -> data_format_trans
+ * (src/runtime_api/core/SimRuntimeCore.cpp:109-147). */
+int hx_load_group(hx_ctx* ctx, const hx_group_desc* desc);
+int hx_get_plan_stats(hx_ctx* ctx, hx_plan_stats* out);
+/* Build the execution plan on the host only (no device needed): validates the
+ * group, reports statistics and checks, on the CPU, that the planned branch
+ * schedule reproduces solve_serial (src/simulate.cpp:558-581) bit for bit on
+ * seeded diagonally dominant systems.  *max_abs_diff receives the largest
+ * difference (0 when bit-exact). */
+int hx_plan_check(const hx_group_desc* desc, int nodes_per_pack, hx_plan_stats* out, double* max_abs_diff);
+
+/* Parameter access in reference instance order (replaces the handle-based
+ * Sim.set/get_variable path, src/python_api/PyBindings.cpp:80-81). */
+int hx_set_param(hx_ctx* ctx, int kind, const double* values, int n);
+int hx_get_param(hx_ctx* ctx, int kind, double* values, int n);
+
+/* ---- forward ------------------------------------------------------------------ */
+/* finitialize(v_init) + nstep fixed steps, recording v at nprobe reference
+ * nodes into trace ((nstep+1) x nprobe, row 0 = initial state).  No tape.
+ * Replaces Simulate::finitialize + Simulate::run (src/simulate.cpp:106-141,
+ * 343-371) and LearnRuntime::simulate_output_vs_into. */
+int hx_simulate(hx_ctx* ctx, int nstep, double v_init, int nprobe, const int* probe_nodes, double* trace);
+/* Same, but also records the forward tape (or its checkpoints) for hx_backward.
+ * Replaces LearnRuntime::simulate_and_capture_mapped_signals_cached
+ * (src/runtime_api/learn/LearnRuntime.cpp:1619-1985). */
+int hx_forward_capture(hx_ctx* ctx, int nstep, double v_init, int nprobe, const int* probe_nodes, double* trace);
+int hx_forward_capture_dev(hx_ctx* ctx, int nstep, double v_init, int nprobe, const int* probe_nodes,
+                           double* trace_dev);
+
+/* ---- backward ------------------------------------------------------------------ */
+/* Exact discrete adjoint of the captured forward.  dLdv: (nstep+1) x nprobe,
+ * dL/d(trace).  grads[kind] (may be NULL per kind) receives dL/d(param) in
+ * reference instance order.  Replaces LearnRuntime::
+ * replay_compute_dw_dx_from_cached_signals_into (LearnRuntime.cpp:1986-2297),
+ * whose LRDS approximation it supersedes. */
+int hx_backward(hx_ctx* ctx, const double* dLdv, double* const* grads);
+int hx_backward_dev(hx_ctx* ctx, const double* dLdv_dev, double* const* grads_dev);
+
+/* Column reduction of per-instance gradients ("MappedSignal" gather +
+ * scatter-add, src/runtime_api/core/kernels/batch_scatter_add.cu:4-27):
+ * out[dest[j]] += scale[j] * grad(kind[j], index[j]); out has n_out floats,
+ * zeroed first.  Must follow hx_backward*. */
+int hx_reduce_grads_f32(hx_ctx* ctx, int n, const int* kind, const int* index, const int32_t* dest,
+                        const float* scale, float* out, int n_out);
+
+/* ---- timing (CUDA events on the launch stream) ---------------------------------- */
+/* Milliseconds of the last forward-capture / backward kernel work, measured with
+ * events recorded around the launches.  which: 0 forward, 1 backward. */
+int hx_last_kernel_ms(hx_ctx* ctx, int which, double* ms, int* launches);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

@@ -1,0 +1,61 @@
+/*
+ * hx_oracle.h -- TEST INFRASTRUCTURE ONLY.
+ *
+ * CPU restatement of the reference's fixed-step forward integrator and a
+ * discrete adjoint of exactly that step sequence.  It is the checker for the
+ * CUDA path: only tests/, __graft_entry__.smoke() and bench.py's CPU-baseline
+ * leg may load it.  The product library never links or calls it.
+ *
+ * Parity pin: the forward is checked bit-for-bit/within 1e-12 against the
+ * reference's own CPU integrator compiled from its sources (oracle/ref_build.sh
+ * -> oracle/_ref/libhxref.so); the adjoint is checked against central finite
+ * differences of that forward (the reference has no exact gradient,
+ * src/runtime_api/learn/LearnRuntime.cpp:208-210).
+ */
+#ifndef HX_ORACLE_H
+#define HX_ORACLE_H
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct hxo_group {
+    int ncell, nnode;
+    const int* parent;            /* -1 for the ncell roots, parent[i] < i otherwise */
+    const double *a, *b, *area, *cm;
+    double celsius, dt;
+    int nhh;
+    const int* hh_node;
+    const double *hh_gnabar, *hh_gkbar, *hh_gl, *hh_el, *hh_ena, *hh_ek;
+    int npas;
+    const int* pas_node;
+    const double *pas_g, *pas_e;
+    int nic;
+    const int* ic_node;
+    const double *ic_del, *ic_dur, *ic_amp;
+} hxo_group;
+
+/* Gradient outputs; any pointer may be NULL.  Each array is per instance of its
+ * mechanism (cm: per node).  Accumulated with '=' (zeroed first). */
+typedef struct hxo_grads {
+    double *hh_gnabar, *hh_gkbar, *hh_gl, *hh_el;
+    double *pas_g, *pas_e;
+    double *cm;
+    double *ic_amp;
+} hxo_grads;
+
+/* Forward: finitialize(v_init) then nstep fadvance steps.
+ * trace: (nstep+1) x nprobe, row 0 = state after finitialize.
+ * v_final (nnode), m/h/n_final (nhh): optional final state. */
+int hxo_forward(const hxo_group* g, double v_init, int nstep, int nprobe, const int* probe,
+                double* trace, double* v_final, double* m_final, double* h_final, double* n_final);
+
+/* Forward + reverse sweep.  dLdv: (nstep+1) x nprobe, dL/d(trace).  The trace of
+ * the forward is written to trace (may be NULL). */
+int hxo_adjoint(const hxo_group* g, double v_init, int nstep, int nprobe, const int* probe,
+                const double* dLdv, double* trace, hxo_grads* grads);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

@@ -1,0 +1,180 @@
+"""ctypes wrapper of the CPU oracle -- TEST INFRASTRUCTURE ONLY.
+
+Only tests/, ``__graft_entry__.smoke()`` and bench.py's CPU-baseline leg may
+import this module; the product package never does.  See ``hx_oracle.h`` for
+what the oracle restates and how it is pinned to the reference.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+import subprocess
+from typing import Dict, Optional, Sequence
+
+import numpy as np
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+_LIB = None
+
+_dp = C.POINTER(C.c_double)
+_ip = C.POINTER(C.c_int)
+
+
+class _Group(C.Structure):
+    _fields_ = [
+        ("ncell", C.c_int),
+        ("nnode", C.c_int),
+        ("parent", _ip),
+        ("a", _dp),
+        ("b", _dp),
+        ("area", _dp),
+        ("cm", _dp),
+        ("celsius", C.c_double),
+        ("dt", C.c_double),
+        ("nhh", C.c_int),
+        ("hh_node", _ip),
+        ("hh_gnabar", _dp),
+        ("hh_gkbar", _dp),
+        ("hh_gl", _dp),
+        ("hh_el", _dp),
+        ("hh_ena", _dp),
+        ("hh_ek", _dp),
+        ("npas", C.c_int),
+        ("pas_node", _ip),
+        ("pas_g", _dp),
+        ("pas_e", _dp),
+        ("nic", C.c_int),
+        ("ic_node", _ip),
+        ("ic_del", _dp),
+        ("ic_dur", _dp),
+        ("ic_amp", _dp),
+    ]
+
+
+class _Grads(C.Structure):
+    _fields_ = [
+        ("hh_gnabar", _dp),
+        ("hh_gkbar", _dp),
+        ("hh_gl", _dp),
+        ("hh_el", _dp),
+        ("pas_g", _dp),
+        ("pas_e", _dp),
+        ("cm", _dp),
+        ("ic_amp", _dp),
+    ]
+
+
+def build() -> str:
+    """Compile the oracle (make) and return the .so path."""
+    subprocess.run(["make", "-s", "-C", _HERE], check=True)
+    return os.path.join(_HERE, "libhxoracle.so")
+
+
+def lib():
+    global _LIB
+    if _LIB is None:
+        path = os.path.join(_HERE, "libhxoracle.so")
+        if not os.path.exists(path):
+            build()
+        L = C.CDLL(path)
+        L.hxo_forward.argtypes = [C.POINTER(_Group), C.c_double, C.c_int, C.c_int, _ip, _dp, _dp, _dp, _dp, _dp]
+        L.hxo_forward.restype = C.c_int
+        L.hxo_adjoint.argtypes = [C.POINTER(_Group), C.c_double, C.c_int, C.c_int, _ip, _dp, _dp, C.POINTER(_Grads)]
+        L.hxo_adjoint.restype = C.c_int
+        _LIB = L
+    return _LIB
+
+
+def _d(x):
+    return x.ctypes.data_as(_dp)
+
+
+def _i(x):
+    return x.ctypes.data_as(_ip)
+
+
+class _Bound:
+    """Keeps numpy arrays alive while the ctypes struct points at them."""
+
+    def __init__(self, g):
+        self.keep = []
+
+        def D(x):
+            x = np.ascontiguousarray(x, dtype=np.float64)
+            self.keep.append(x)
+            return _d(x)
+
+        def I(x):
+            x = np.ascontiguousarray(x, dtype=np.int32)
+            self.keep.append(x)
+            return _i(x)
+
+        s = _Group()
+        s.ncell = g.ncell
+        s.nnode = g.nnode
+        s.parent = I(g.parent)
+        s.a, s.b, s.area, s.cm = D(g.a), D(g.b), D(g.area), D(g.cm)
+        s.celsius = g.celsius
+        s.dt = g.dt
+        h = g.hh
+        s.nhh = h.n
+        s.hh_node = I(h.nodes)
+        s.hh_gnabar, s.hh_gkbar, s.hh_gl, s.hh_el = (D(h.fields[k]) for k in ("gnabar", "gkbar", "gl", "el"))
+        s.hh_ena, s.hh_ek = D(h.fields["ena"]), D(h.fields["ek"])
+        p = g.pas
+        s.npas = p.n
+        s.pas_node = I(p.nodes)
+        s.pas_g, s.pas_e = D(p.fields["g"]), D(p.fields["e"])
+        c = g.iclamp
+        s.nic = c.n
+        s.ic_node = I(c.nodes)
+        s.ic_del, s.ic_dur, s.ic_amp = D(c.fields["del"]), D(c.fields["dur"]), D(c.fields["amp"])
+        self.s = s
+
+
+def forward(g, nstep: int, probe: Optional[Sequence[int]] = None, v_init: Optional[float] = None):
+    """Run finitialize + nstep steps; returns (trace[(nstep+1), nprobe], final_state dict)."""
+    L = lib()
+    probe = np.ascontiguousarray(g.soma_nodes() if probe is None else probe, dtype=np.int32)
+    b = _Bound(g)
+    trace = np.zeros((nstep + 1, probe.shape[0]))
+    vf = np.zeros(g.nnode)
+    nh = max(g.hh.n, 1)
+    mf, hf, nf = np.zeros(nh), np.zeros(nh), np.zeros(nh)
+    rc = L.hxo_forward(C.byref(b.s), float(g.v_init if v_init is None else v_init), int(nstep), int(probe.shape[0]),
+                       _i(probe), _d(trace), _d(vf), _d(mf), _d(hf), _d(nf))
+    if rc != 0:
+        raise RuntimeError("oracle forward failed")
+    return trace, {"v": vf, "m": mf[: g.hh.n], "h": hf[: g.hh.n], "n": nf[: g.hh.n]}
+
+
+GRAD_KEYS = ("hh.gnabar", "hh.gkbar", "hh.gl", "hh.el", "pas.g", "pas.e", "cm", "IClamp.amp")
+
+
+def adjoint(g, nstep: int, dLdv: np.ndarray, probe: Optional[Sequence[int]] = None, v_init: Optional[float] = None):
+    """Forward + reverse sweep; returns (trace, grads dict keyed by GRAD_KEYS)."""
+    L = lib()
+    probe = np.ascontiguousarray(g.soma_nodes() if probe is None else probe, dtype=np.int32)
+    dLdv = np.ascontiguousarray(dLdv, dtype=np.float64)
+    if dLdv.shape != (nstep + 1, probe.shape[0]):
+        raise ValueError("dLdv must have shape (nstep+1, nprobe)")
+    b = _Bound(g)
+    trace = np.zeros((nstep + 1, probe.shape[0]))
+    out: Dict[str, np.ndarray] = {
+        "hh.gnabar": np.zeros(g.hh.n),
+        "hh.gkbar": np.zeros(g.hh.n),
+        "hh.gl": np.zeros(g.hh.n),
+        "hh.el": np.zeros(g.hh.n),
+        "pas.g": np.zeros(g.pas.n),
+        "pas.e": np.zeros(g.pas.n),
+        "cm": np.zeros(g.nnode),
+        "IClamp.amp": np.zeros(g.iclamp.n),
+    }
+    gs = _Grads()
+    gs.hh_gnabar, gs.hh_gkbar, gs.hh_gl, gs.hh_el = (_d(out[k]) for k in GRAD_KEYS[:4])
+    gs.pas_g, gs.pas_e, gs.cm, gs.ic_amp = (_d(out[k]) for k in GRAD_KEYS[4:])
+    rc = L.hxo_adjoint(C.byref(b.s), float(g.v_init if v_init is None else v_init), int(nstep), int(probe.shape[0]),
+                       _i(probe), _d(dLdv), _d(trace), C.byref(gs))
+    if rc != 0:
+        raise RuntimeError("oracle adjoint failed")
+    return trace, out

@@ -1,0 +1,163 @@
+"""GPU parity of the CUDA path against the CPU oracle (through the C ABI).
+
+Tolerances: voltages within 1e-9 relative to the trace's
+scale (max |v_ref|), parameter gradients within 1e-7 relative to the largest
+reference gradient of the same kind, spike counts identical with spike times
+within one dt.
+"""
+import numpy as np
+import pytest
+
+from heliox_b200 import synth
+from oracle import oracle as O
+
+pytestmark = pytest.mark.gpu
+
+V_TOL = 1e-9
+G_TOL = 1e-7
+
+
+@pytest.fixture(scope="module")
+def Sim():
+    from heliox_b200.runtime import Sim as S
+
+    return S
+
+
+def _spikes(tr, dt):
+    up = (tr[1:] > 0.0) & (tr[:-1] <= 0.0)
+    return [np.nonzero(up[:, j])[0] * dt for j in range(tr.shape[1])]
+
+
+def _check_v(tr_gpu, tr_ref, dt):
+    scale = np.max(np.abs(tr_ref))
+    err = np.max(np.abs(tr_gpu - tr_ref)) / scale
+    assert err <= V_TOL, err
+    for sg, sr in zip(_spikes(tr_gpu, dt), _spikes(tr_ref, dt)):
+        assert len(sg) == len(sr)
+        if len(sr):
+            assert np.max(np.abs(sg - sr)) <= dt
+
+
+def _check_g(gg, gr, keys):
+    for k in keys:
+        ref = gr[k]
+        if ref.size == 0:
+            continue
+        scale = np.max(np.abs(ref))
+        err = np.max(np.abs(gg[k] - ref)) / max(scale, 1e-300)
+        assert err <= G_TOL, (k, err)
+
+
+def test_forward_ball_and_stick(Sim):
+    g = synth.ball_and_stick()
+    s = Sim(0)
+    s.load_group(g)
+    probes = np.array([0, 1, 50, 100], dtype=np.int32)
+    tr = s.simulate(4000, probes=probes)
+    ref, _ = O.forward(g, 4000, probe=probes)
+    _check_v(tr, ref, g.dt)
+    assert len(_spikes(ref[:, :1], g.dt)[0]) >= 3
+
+
+def test_forward_random_trees(Sim):
+    g = synth.random_tree_batch(12, seed0=101)
+    s = Sim(0, pack_target=1500)
+    s.load_group(g)
+    rng = np.random.default_rng(0)
+    probes = np.concatenate([g.soma_nodes(), rng.integers(g.ncell, g.nnode, 8)]).astype(np.int32)
+    tr = s.simulate(4000, probes=probes)
+    ref, _ = O.forward(g, 4000, probe=probes)
+    _check_v(tr, ref, g.dt)
+
+
+def test_capture_trace_equals_simulate(Sim):
+    g = synth.random_tree_batch(4, seed0=7)
+    s = Sim(0)
+    s.load_group(g)
+    a = s.simulate(800)
+    b = s.forward_capture(800)
+    assert np.array_equal(a, b)
+
+
+def test_backward_ball_and_stick_mse(Sim):
+    g = synth.ball_and_stick()
+    target, _ = O.forward(synth.ball_and_stick(gnabar_scale=1.1), 4000)
+    s = Sim(0)
+    s.load_group(g)
+    tr = s.forward_capture(4000)
+    T = 4000
+    dLdv = np.zeros_like(tr)
+    dLdv[1:] = 2.0 * (tr[1:] - target[1:]) / T
+    gg = s.backward(dLdv)
+    _, gr = O.adjoint(g, T, dLdv)
+    _check_g(gg, gr, O.GRAD_KEYS)
+
+
+def test_backward_random_trees(Sim):
+    g = synth.random_tree_batch(6, seed0=55)
+    T = 2000
+    s = Sim(0)
+    s.load_group(g)
+    tr = s.forward_capture(T)
+    rng = np.random.default_rng(5)
+    dLdv = rng.standard_normal(tr.shape) * 1e-3
+    gg = s.backward(dLdv)
+    ref_tr, gr = O.adjoint(g, T, dLdv)
+    _check_v(tr, ref_tr, g.dt)
+    _check_g(gg, gr, O.GRAD_KEYS)
+
+
+def test_checkpointed_backward_equals_full_tape(Sim):
+    g = synth.random_tree_batch(5, seed0=21)
+    T = 1000
+    rng = np.random.default_rng(9)
+    full = Sim(0)
+    full.load_group(g)
+    tr = full.forward_capture(T)
+    dLdv = rng.standard_normal(tr.shape)
+    g_full = full.backward(dLdv)
+    per_step = (g.nnode + 3 * g.hh.n) * 8
+    ck = Sim(0, tape_budget_bytes=per_step * 80)
+    ck.load_group(g)
+    tr2 = ck.forward_capture(T)
+    g_ck = ck.backward(dLdv)
+    assert np.array_equal(tr, tr2)
+    for k in g_full:
+        assert np.array_equal(g_full[k], g_ck[k]), k
+
+
+def test_param_roundtrip_and_effect(Sim):
+    g = synth.random_tree_batch(3, seed0=2)
+    s = Sim(0)
+    s.load_group(g)
+    x = s.get_param_array("hh.gnabar")
+    assert np.array_equal(x, g.hh.fields["gnabar"])
+    y = x * 1.05
+    s.set_param_array("hh.gnabar", y)
+    assert np.array_equal(s.get_param_array("hh.gnabar"), y)
+    g2 = g.copy()
+    g2.hh.fields["gnabar"] = y
+    tr = s.simulate(600)
+    ref, _ = O.forward(g2, 600)
+    _check_v(tr, ref, g.dt)
+
+
+def test_reduce_grads_columns(Sim):
+    g = synth.random_tree_batch(3, seed0=4)
+    s = Sim(0)
+    s.load_group(g)
+    tr = s.forward_capture(500)
+    dLdv = np.ones_like(tr) * 1e-2
+    gg = s.backward(dLdv)
+    rng = np.random.default_rng(2)
+    n = 50
+    idx = rng.integers(0, g.hh.n, n)
+    handles = [s.get_variable_handle("hh", "gnabar", int(i)) for i in idx]
+    dest = rng.integers(0, 7, n).astype(np.int32)
+    scale = rng.uniform(0.5, 2, n).astype(np.float32)
+    out = s.reduce_grads_f32(handles, dest, scale, 7)
+    ref = np.zeros(7)
+    for j in range(n):
+        ref[dest[j]] += float(scale[j]) * gg["hh.gnabar"][idx[j]]
+    np.testing.assert_allclose(out, ref.astype(np.float32), rtol=1e-6, atol=1e-30)

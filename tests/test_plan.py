@@ -1,0 +1,91 @@
+"""CPU: the host planner (cell packing + branch-level Hines schedule).
+
+``hx_plan_check`` builds the execution plan the kernels use and replays the
+planned triangularisation/back-substitution order on the CPU; it must equal the
+reference's solve_serial (src/simulate.cpp:558-581) bit for bit, for the
+forward and the transposed system.
+"""
+import numpy as np
+import pytest
+
+from heliox_b200 import _lib, synth
+from heliox_b200.model import CellGroup, MechTable, _f64, _i32, concat_groups
+
+
+def _chain_group(n, ncell=1):
+    cells = []
+    for c in range(ncell):
+        parent = np.arange(-1, n - 1, dtype=np.int32)
+        g = CellGroup(
+            ncell=1,
+            parent=parent,
+            a=_f64(-np.linspace(1, 2, n)),
+            b=_f64(-np.linspace(2, 3, n)),
+            area=_f64(np.full(n, 100.0)),
+            cm=_f64(np.ones(n)),
+            hh=MechTable(_i32([0]), {k: _f64([v]) for k, v in synth.HH_STD.items()}),
+            pas=MechTable(_i32(np.arange(1, n)), {"g": _f64(np.full(n - 1, 1e-4)), "e": _f64(np.full(n - 1, -65.0))}),
+            iclamp=MechTable(_i32([]), {k: _f64([]) for k in ("del", "dur", "amp")}),
+        )
+        cells.append(g)
+    return concat_groups(cells) if ncell > 1 else cells[0]
+
+
+def _star_group(arms=40, arm_len=3):
+    parent = [-1]
+    for a in range(arms):
+        prev = 0
+        for j in range(arm_len):
+            parent.append(prev)
+            prev = len(parent) - 1
+    n = len(parent)
+    rng = np.random.default_rng(0)
+    return CellGroup(
+        ncell=1,
+        parent=_i32(parent),
+        a=_f64(-rng.uniform(1, 3, n)),
+        b=_f64(-rng.uniform(1, 3, n)),
+        area=_f64(np.full(n, 50.0)),
+        cm=_f64(np.ones(n)),
+        hh=MechTable(_i32([0]), {k: _f64([v]) for k, v in synth.HH_STD.items()}),
+        pas=MechTable(_i32([]), {"g": _f64([]), "e": _f64([])}),
+        iclamp=MechTable(_i32([]), {k: _f64([]) for k in ("del", "dur", "amp")}),
+    )
+
+
+@pytest.mark.parametrize(
+    "maker,target",
+    [
+        (lambda: synth.ball_and_stick(), 0),
+        (lambda: _chain_group(1), 0),
+        (lambda: _chain_group(2), 0),
+        (lambda: _chain_group(7, ncell=5), 0),
+        (lambda: _star_group(), 0),
+        (lambda: synth.random_tree_batch(24, seed0=11), 0),
+        (lambda: synth.random_tree_batch(24, seed0=11), 4096),
+        (lambda: synth.random_tree_cell(3, ncomp=3000, max_levels=40), 0),
+    ],
+)
+def test_planned_solve_bit_exact(maker, target):
+    g = maker()
+    stats, diff = _lib.plan_check(g, target)
+    assert diff == 0.0
+    assert stats["npack"] >= 1
+    assert stats["max_pack_nodes"] >= 1
+
+
+def test_packing_balance_and_coverage():
+    g = synth.random_tree_batch(96, seed0=3)
+    stats, diff = _lib.plan_check(g, 1024)
+    assert diff == 0.0
+    assert stats["imbalance"] < 1.35
+    assert stats["nbranch"] >= g.ncell
+
+
+def test_invalid_group_rejected():
+    g = synth.ball_and_stick()
+    bad = g.copy()
+    bad.parent = bad.parent.copy()
+    bad.parent[5] = 7  # parent after child
+    with pytest.raises(ValueError):
+        _lib.plan_check(bad)
