@@ -89,7 +89,7 @@ SIGNATURES = {
     "hx_set_tape_budget": (C.c_int, [C.c_void_p, C.c_size_t]),
     "hx_load_group": (C.c_int, [C.c_void_p, C.POINTER(GroupDesc)]),
     "hx_get_plan_stats": (C.c_int, [C.c_void_p, C.POINTER(PlanStats)]),
-    "hx_plan_check": (C.c_int, [C.POINTER(GroupDesc), C.c_int, C.POINTER(PlanStats), _dp]),
+    "hx_plan_check": (C.c_int, [C.POINTER(GroupDesc), C.c_int, C.POINTER(PlanStats), _dp, _dp]),
     "hx_set_param": (C.c_int, [C.c_void_p, C.c_int, _dp, C.c_int]),
     "hx_get_param": (C.c_int, [C.c_void_p, C.c_int, _dp, C.c_int]),
     "hx_simulate": (C.c_int, [C.c_void_p, C.c_int, C.c_double, C.c_int, _ip, _dp]),
@@ -175,7 +175,10 @@ def plan_check(g, nodes_per_pack: int = 0):
     b = BoundGroup(g)
     st = PlanStats()
     diff = C.c_double(-1.0)
-    rc = L.hx_plan_check(C.byref(b.desc), int(nodes_per_pack), C.byref(st), C.byref(diff))
+    pq = C.c_double(-1.0)
+    rc = L.hx_plan_check(C.byref(b.desc), int(nodes_per_pack), C.byref(st), C.byref(diff), C.byref(pq))
     if rc != 0:
         raise ValueError(f"hx_plan_check failed (rc={rc})")
-    return st.as_dict(), float(diff.value)
+    d = st.as_dict()
+    d["pq_rel_diff"] = float(pq.value)
+    return d, float(diff.value)

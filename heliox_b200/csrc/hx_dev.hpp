@@ -5,16 +5,22 @@
 
 namespace hx {
 
-constexpr int kThreads = 256;  // threads per CTA (one CTA per cell pack)
+constexpr int kThreads = 256;  // threads per CTA (one CTA per cell pack, 8 warps)
 
-// The execution plan and the model parameters, GPU (pack-contiguous) order.
+enum NodeFlag : int { kHasPas = 1, kHasHH = 2 };
+
+// The execution plan and the model parameters.  Node arrays are in GPU
+// (pack-contiguous, cell-contiguous) order; density-mechanism parameters are
+// node-indexed (zero where the mechanism is absent, selected by node_flags).
 struct DevGroup {
-    int npack, nnode, nhh, npas, nic;
-    int smem_n, smem_nh;  // shared-memory array strides (max pack nodes / hh instances)
-    const int *pack_node_off, *pack_hh_off, *pack_br_off, *pack_lvl_off, *pack_nlev, *level_br_off;
+    int npack, nnode, nic;
+    // shared-memory table sizes (maxima over packs)
+    int smem_n, smem_br, smem_bch, smem_nch, smem_lvl;
+    const int *pack_node_off, *pack_slot_off, *pack_br_off, *pack_bch_off, *pack_nch_off;
+    const int *cs_node0, *cs_nnode, *cs_warp0, *cs_nwarp, *cs_bar, *cs_lvl_off, *cs_nlev;
+    const int* level_br_off;
     const int *br_head, *br_end, *br_parent, *br_child_off, *br_child;
-    const int *node_parent, *node_child_off, *node_child;
-    const int *node_hh, *node_pas, *node_ic_off, *node_ic;
+    const int *node_parent, *node_child_off, *node_child, *node_flags, *node_ic_off, *node_ic;
     const double *a, *b, *cm, *area;
     const double *hh_gnabar, *hh_gkbar, *hh_gl, *hh_el, *hh_ena, *hh_ek;
     const double *pas_g, *pas_e;
@@ -22,15 +28,16 @@ struct DevGroup {
     double dt, cfac, q10;
 };
 
-// Simulation state in global memory (between windows).
+// Simulation state in global memory (between windows); gates node-indexed.
 struct DevState {
     double *v, *m, *h, *n;
 };
 
-// Forward tape: state at the start of step k lives in row (k - k_base).
+// Forward tape: state at the start of step k lives in row (k - k_base); every
+// row holds nnode values of v and of each gate.
 struct DevTape {
-    double* v;           // rows x nnode
-    double *m, *h, *n;   // rows x nhh
+    double* v;
+    double *m, *h, *n;
     int k_base;
 };
 
@@ -42,11 +49,12 @@ struct DevProbe {
     int nprobe;
 };
 
-// Adjoint state (between windows) and gradient accumulators (GPU order).
+// Adjoint state (between windows), node-indexed.
 struct DevAdj {
     double *lv, *lm, *lh, *ln;
 };
 
+// Gradient accumulators: node-indexed except ic_amp (per IClamp instance).
 struct DevGrad {
     double *hh_gnabar, *hh_gkbar, *hh_gl, *hh_el;
     double *pas_g, *pas_e, *cm, *ic_amp;

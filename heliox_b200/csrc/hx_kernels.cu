@@ -1,17 +1,19 @@
 // hx_kernels.cu -- fused per-timestep kernels for sm_100a (fp64).
 //
 // One CTA owns one cell pack for a whole window of timesteps: voltages, the
-// Hines matrix (d, rhs), the axial coefficients and the hh gates stay in shared
-// memory across steps; only the forward tape, the recorded probes and the
-// mechanism parameters (L2-resident) touch global memory inside the loop.
+// Hines work arrays, the hh gates and the pack's topology/schedule tables stay
+// in shared memory across steps; only the forward tape, the recorded probes and
+// the node parameters (L2-resident) touch global memory inside the loop.  Each
+// cell of the pack is advanced by its own group of warps, synchronised by a
+// named barrier, so the serial parts of one cell's Hines solve overlap the
+// mechanism arithmetic of the other cells on the same SM.
 //
 // Forward step (reference: Simulate::fadvance_cpu, src/simulate.cpp:410-442):
 //   A  node-parallel: mechanism currents with the finite-difference
 //      conductance (mech_template.cuh:589-648), capacitance jacobian
 //      (capac.cpp:68-78) and the axial terms (simulate.cpp:542-555) gathered
 //      per node in the order the reference's scatter loop applies them;
-//   B  Hines solve, one thread per unbranched chain, levels deepest-first then
-//      root-first (solve_serial, simulate.cpp:558-581, reproduced bit for bit);
+//   B  Hines solve on the branch-level schedule (hines_smem below);
 //   C  v += dv (update_cpu, simulate.cpp:759-770), then the hh cnexp state
 //      update at the new voltage (nonvint_cpu, simulate.cpp:784-852).
 // Backward step: the transpose of the above, in reverse (no reference
@@ -24,351 +26,524 @@
 
 namespace hx {
 
-// ------------------------------------------------------------------ init
-__global__ void init_state_kernel(DevGroup G, DevState S, double v_init) {
-    const int i = blockIdx.x * blockDim.x + threadIdx.x;
-    if (i < G.nnode) S.v[i] = v_init;
-    if (i < G.nhh) {
-        HHRates r;
-        hh_rates(v_init, G.q10, r);  // hh INITIAL: gates at steady state (hh_templated.cu:111-122)
-        S.m[i] = r.minf;
-        S.h[i] = r.hinf;
-        S.n[i] = r.ninf;
+// ------------------------------------------------------------------ Hines (shared memory)
+// hines_cell (below) solves one cell's tree system in place: d (diagonal in,
+// reciprocal of the eliminated diagonal out), rhs (right-hand side in, solution
+// out).  sa/sb are the axial coefficients in shared memory; A eliminates a
+// child into its parent and U couples a node to its parent (forward: A=a, U=b;
+// transposed system: A=b, U=a).
+//
+// The reference eliminates with a division on every step of the chain
+// (solve_serial, simulate.cpp:558-581).  Here the eliminated diagonal and rhs
+// of an unbranched chain are carried in projective form (tri_block below), so
+// the serial dependencies are FMAs only; exact power-of-two rescaling keeps
+// p, q, y in range and the reciprocals are formed off the chains with a
+// branch-free Newton reciprocal.  The back-substitution is one FMA per node.
+__device__ __forceinline__ double rescale_pow2(double x) {
+    // 2^-floor(log2 x) for positive normal x; exact
+    const long long e = ((__double_as_longlong(x) >> 52) & 0x7FF);
+    return __longlong_as_double((2046LL - e) << 52);
+}
+
+// Register-blocked chain kernels.  Every block loads up to kBlk nodes' operands
+// from shared memory into registers before the dependent arithmetic and stores
+// the results afterwards, so that no shared-memory load waits behind a store
+// of the same array on the critical path.  cnt <= kBlk nodes are processed;
+// callers pass kBlk for full blocks.
+constexpr int kBlk = 4;
+
+// tri_block: triangularisation of a chain from node j downwards in projective
+// form.  With d'_k = p_k/q_k and the eliminated rhs r'_k = y_k/q_k:
+//   p_{k-1} = d_{k-1} p_k - A_k U_k q_k,   q_{k-1} = p_k,
+//   y_{k-1} = rhs_{k-1} p_k - A_k y_k,
+// two FMA chains without division.  For k = j .. j-cnt+1 it stores
+// d[k] = 1/d'_k = q_k/p_k and rhs[k] = r'_k/d'_k = y_k/p_k (the reciprocal is
+// off both chains) and leaves (p, q, y) of node j-cnt.
+template <bool kGuard>
+__device__ __forceinline__ void tri_block(double* __restrict__ d, double* __restrict__ rhs,
+                                          const double* __restrict__ A, const double* __restrict__ U, int j, int cnt,
+                                          double& pp, double& qq, double& yy) {
+    double dl[kBlk], rl[kBlk], al[kBlk], cl[kBlk], pv[kBlk], qv[kBlk], yv[kBlk];
+#pragma unroll
+    for (int u = 0; u < kBlk; ++u) {
+        if (!kGuard || u < cnt) {
+            dl[u] = d[j - 1 - u];
+            rl[u] = rhs[j - 1 - u];
+            al[u] = A[j - u];
+            cl[u] = al[u] * U[j - u];
+        }
+    }
+#pragma unroll
+    for (int u = 0; u < kBlk; ++u) {
+        if (!kGuard || u < cnt) {
+            pv[u] = pp;
+            qv[u] = qq;
+            yv[u] = yy;
+            const double pn = __fma_rn(dl[u], pp, -(cl[u] * qq));
+            const double yn = __fma_rn(rl[u], pp, -(al[u] * yy));
+            qq = pp;
+            pp = pn;
+            yy = yn;
+        }
+    }
+#pragma unroll
+    for (int u = 0; u < kBlk; ++u) {
+        if (!kGuard || u < cnt) {
+            const double ip = rcp_pos(pv[u]);
+            d[j - u] = qv[u] * ip;
+            rhs[j - u] = yv[u] * ip;
+        }
     }
 }
 
-// ------------------------------------------------------------------ Hines (shared memory)
-// Triangularise + back-substitute the pack's tree system.  A = coefficient
-// eliminating a child into its parent, U = coupling of a node to its parent
-// (forward: A=a, U=b; transposed system: A=b, U=a).
-__device__ __forceinline__ void hines_smem(const DevGroup& G, int p, const double* __restrict__ A,
-                                           const double* __restrict__ U, double* __restrict__ d,
-                                           double* __restrict__ rhs) {
-    const int bb = G.pack_br_off[p];
-    const int* lo = G.level_br_off + G.pack_lvl_off[p];
-    const int nlev = G.pack_nlev[p];
-    for (int L = nlev - 1; L >= 0; --L) {
-        const int b0 = lo[L], b1 = lo[L + 1];
-        for (int br = b0 + (int)threadIdx.x; br < b1; br += blockDim.x) {
-            const int gb = bb + br;
-            const int h = G.br_head[gb], e = G.br_end[gb];
-            double de = d[e], re = rhs[e];
-            // child branches fold into the branch end in descending reference index
-            for (int k = G.br_child_off[gb]; k < G.br_child_off[gb + 1]; ++k) {
-                const int c = G.br_child[k];
-                const double f = A[c] / d[c];
-                de = de - f * U[c];
-                re = re - f * rhs[c];
-            }
-            for (int j = e; j > h; --j) {
-                d[j] = de;
-                rhs[j] = re;
-                const double f = A[j] / de;
-                de = d[j - 1] - f * U[j];
-                re = rhs[j - 1] - f * re;
-            }
-            d[h] = de;
-            rhs[h] = re;
+// back_block: x_k = rhs'_k/d'_k - (U_k/d'_k) x_{k-1} for k = j .. j+cnt-1
+// (d holds 1/d'_k, rhs holds rhs'_k/d'_k); one FMA per node on the chain.
+template <bool kGuard>
+__device__ __forceinline__ void back_block(const double* __restrict__ d, double* __restrict__ rhs,
+                                           const double* __restrict__ U, int j, int cnt, double& x) {
+    double hl[kBlk], gl[kBlk];
+#pragma unroll
+    for (int u = 0; u < kBlk; ++u) {
+        if (!kGuard || u < cnt) {
+            hl[u] = U[j + u] * d[j + u];
+            gl[u] = rhs[j + u];
         }
-        __syncthreads();
     }
-    for (int L = 0; L < nlev; ++L) {
-        const int b0 = lo[L], b1 = lo[L + 1];
-        for (int br = b0 + (int)threadIdx.x; br < b1; br += blockDim.x) {
-            const int gb = bb + br;
-            const int h = G.br_head[gb], e = G.br_end[gb];
-            const int par = G.br_parent[gb];
-            double x = rhs[h];
-            if (par >= 0) x = x - U[h] * rhs[par];
-            x = x / d[h];
-            rhs[h] = x;
-            for (int j = h + 1; j <= e; ++j) {
-                x = (rhs[j] - U[j] * x) / d[j];
-                rhs[j] = x;
-            }
+#pragma unroll
+    for (int u = 0; u < kBlk; ++u) {
+        if (!kGuard || u < cnt) {
+            x = __fma_rn(-hl[u], x, gl[u]);
+            gl[u] = x;
         }
-        __syncthreads();
+    }
+#pragma unroll
+    for (int u = 0; u < kBlk; ++u)
+        if (!kGuard || u < cnt) rhs[j + u] = gl[u];
+}
+
+// ------------------------------------------------------------------ cell groups
+// Shared-memory copies of the pack's topology and schedule (int tables).
+struct Meta {
+    int* par;   // node parent (pack-local), -1 for roots
+    int* flag;  // NodeFlag bits
+    int* cho;   // node child offsets into ch (size n+1)
+    int* ch;    // node children (pack-local), ascending reference index
+    int* bh;    // branch head / end / head's parent (pack-local nodes)
+    int* be;
+    int* bp;
+    int* bco;   // branch child offsets into bc (size nbr+1)
+    int* bc;    // child-branch heads, descending reference index
+    int* lvl;   // level tables of the pack's cells (pack-local branch ids)
+};
+
+// One cell and the warps of the CTA that own it.
+struct Grp {
+    int nb, n;       // pack-local first node, node count
+    int tl, nt;      // thread index inside the group, group size
+    int bar, nwarp;  // named barrier id (multi-warp groups)
+    int lvl, nlev;   // offset of the cell's level table in Meta::lvl, levels
+    __device__ __forceinline__ void sync() const {
+        if (nwarp == 1)
+            __syncwarp();
+        else
+            asm volatile("bar.sync %0, %1;" ::"r"(bar), "r"(nt) : "memory");
+    }
+};
+
+__device__ __forceinline__ size_t meta_ints(const DevGroup& G) {
+    return 3 * (size_t)G.smem_n + 1 + G.smem_nch + 4 * (size_t)G.smem_br + 1 + G.smem_bch + G.smem_lvl;
+}
+
+// Loads the pack's tables into shared memory (whole CTA), then returns the
+// calling thread's cell group; false for warps the pack leaves idle.
+__device__ __forceinline__ bool setup_pack(const DevGroup& G, int p, int* ibase, Meta& M, Grp& g) {
+    const int tid = threadIdx.x, nt = blockDim.x;
+    M.par = ibase;
+    M.flag = M.par + G.smem_n;
+    M.cho = M.flag + G.smem_n;
+    M.ch = M.cho + G.smem_n + 1;
+    M.bh = M.ch + G.smem_nch;
+    M.be = M.bh + G.smem_br;
+    M.bp = M.be + G.smem_br;
+    M.bco = M.bp + G.smem_br;
+    M.bc = M.bco + G.smem_br + 1;
+    M.lvl = M.bc + G.smem_bch;
+    const int pb = G.pack_node_off[p], pn = G.pack_node_off[p + 1] - pb;
+    const int nch0 = G.pack_nch_off[p], nch = G.pack_nch_off[p + 1] - nch0;
+    const int br0 = G.pack_br_off[p], nbr = G.pack_br_off[p + 1] - br0;
+    const int bc0 = G.pack_bch_off[p], nbc = G.pack_bch_off[p + 1] - bc0;
+    const int s0 = G.pack_slot_off[p], s1 = G.pack_slot_off[p + 1];
+    const int l0 = G.cs_lvl_off[s0], l1 = G.cs_lvl_off[s1 - 1] + G.cs_nlev[s1 - 1] + 1;
+    for (int i = tid; i < pn; i += nt) {
+        M.par[i] = G.node_parent[pb + i];
+        M.flag[i] = G.node_flags[pb + i];
+        M.cho[i] = G.node_child_off[pb + i] - nch0;
+    }
+    if (tid == 0) M.cho[pn] = nch;
+    for (int k = tid; k < nch; k += nt) M.ch[k] = G.node_child[nch0 + k];
+    for (int k = tid; k < nbr; k += nt) {
+        M.bh[k] = G.br_head[br0 + k];
+        M.be[k] = G.br_end[br0 + k];
+        M.bp[k] = G.br_parent[br0 + k];
+        M.bco[k] = G.br_child_off[br0 + k] - bc0;
+    }
+    if (tid == 0) M.bco[nbr] = nbc;
+    for (int k = tid; k < nbc; k += nt) M.bc[k] = G.br_child[bc0 + k];
+    for (int k = tid; k < l1 - l0; k += nt) M.lvl[k] = G.level_br_off[l0 + k];
+    __syncthreads();
+    const int w = tid >> 5;
+    for (int s = s0; s < s1; ++s) {
+        const int w0 = G.cs_warp0[s], nw = G.cs_nwarp[s];
+        if (w >= w0 && w < w0 + nw) {
+            g.nb = G.cs_node0[s];
+            g.n = G.cs_nnode[s];
+            g.tl = tid - 32 * w0;
+            g.nt = 32 * nw;
+            g.bar = G.cs_bar[s];
+            g.nwarp = nw;
+            g.lvl = G.cs_lvl_off[s] - l0;
+            g.nlev = G.cs_nlev[s];
+            return true;
+        }
+    }
+    return false;
+}
+
+template <bool kTransposed>
+__device__ __forceinline__ void hines_cell(const Meta& M, const Grp& g, const double* __restrict__ sa,
+                                           const double* __restrict__ sb, double* __restrict__ d,
+                                           double* __restrict__ rhs) {
+    const double* __restrict__ A = kTransposed ? sb : sa;
+    const double* __restrict__ U = kTransposed ? sa : sb;
+    const int* lo = M.lvl + g.lvl;
+    for (int L = g.nlev - 1; L >= 0; --L) {
+        const int b1 = lo[L + 1];
+        for (int br = lo[L] + g.tl; br < b1; br += g.nt) {
+            const int h = M.bh[br], e = M.be[br];
+            double de = d[e], re = rhs[e];
+            // child branches fold into the end node (d[c] = 1/d'_c, rhs[c] = r'_c/d'_c)
+            const int c1 = M.bco[br + 1];
+            for (int k = M.bco[br]; k < c1; ++k) {
+                const int c = M.bc[k];
+                de = __fma_rn(-(A[c] * U[c]), d[c], de);
+                re = __fma_rn(-A[c], rhs[c], re);
+            }
+            double pp = de, qq = 1.0, yy = re;
+            int j = e;
+            for (; j - h >= kBlk; j -= kBlk) {
+                tri_block<false>(d, rhs, A, U, j, kBlk, pp, qq, yy);
+                const double s = rescale_pow2(pp);
+                pp *= s;
+                qq *= s;
+                yy *= s;
+            }
+            if (j > h) tri_block<true>(d, rhs, A, U, j, j - h, pp, qq, yy);
+            const double ip = rcp_pos(pp);
+            d[h] = qq * ip;
+            rhs[h] = yy * ip;
+        }
+        g.sync();
+    }
+    for (int L = 0; L < g.nlev; ++L) {
+        const int b1 = lo[L + 1];
+        for (int br = lo[L] + g.tl; br < b1; br += g.nt) {
+            const int h = M.bh[br], e = M.be[br];
+            const int par = M.bp[br];
+            double x = rhs[h];
+            if (par >= 0) x = __fma_rn(-(U[h] * d[h]), rhs[par], x);
+            rhs[h] = x;
+            int j = h + 1;
+            for (; e - j + 1 >= kBlk; j += kBlk) back_block<false>(d, rhs, U, j, kBlk, x);
+            if (j <= e) back_block<true>(d, rhs, U, j, e - j + 1, x);
+        }
+        g.sync();
     }
 }
 
 // ------------------------------------------------------------------ assembly
-// rhs/d of node i (pack-local) in the reference's accumulation order:
+// rhs/d of pack-local node i in the reference's accumulation order:
 // pas, hh, IClamp (CoreNEURON type order), capacitance jacobian, axial terms.
 template <bool kRhs>
-__device__ __forceinline__ void assemble(const DevGroup& G, int nb, int hb, int i, const double* __restrict__ sv,
-                                         const double* __restrict__ sa, const double* __restrict__ sb, int jh,
-                                         double m, double h, double n, double tmid, double& r_out, double& d_out) {
-    const int gi = nb + i;
+__device__ __forceinline__ void assemble(const DevGroup& G, const Meta& M, int pb, int i, int fl,
+                                         const double* __restrict__ sv, const double* __restrict__ sa,
+                                         const double* __restrict__ sb, double m, double h, double n, double tmid,
+                                         double& r_out, double& d_out) {
+    const int gi = pb + i;
     const double vi = sv[i];
     double r = 0.0, dd = 0.0;
-    const int jp = G.node_pas[gi];
-    if (jp >= 0) {  // pas_templated.cu:27-31 through MechTemp::current (FD conductance)
-        const double g = G.pas_g[jp], e = G.pas_e[jp];
+    if (fl & kHasPas) {  // pas_templated.cu:27-31 through MechTemp::current (FD conductance)
+        const double g = __ldg(G.pas_g + gi), e = __ldg(G.pas_e + gi);
         double g1 = g * ((vi + kFdEps) - e);
         const double i0 = g * (vi - e);
-        g1 = (g1 - i0) / kFdEps;
+        g1 = (g1 - i0) * kInvFdEps;
         r -= i0;
         dd += g1;
     }
-    if (jh >= 0) {  // hh_templated.cu:137-149
-        const int gj = hb + jh;
-        const double gnabar = G.hh_gnabar[gj], gkbar = G.hh_gkbar[gj], gl = G.hh_gl[gj];
-        const double ena = G.hh_ena[gj], ek = G.hh_ek[gj], el = G.hh_el[gj];
+    if (fl & kHasHH) {  // hh_templated.cu:137-149
+        const double gnabar = __ldg(G.hh_gnabar + gi), gkbar = __ldg(G.hh_gkbar + gi), gl = __ldg(G.hh_gl + gi);
+        const double ena = __ldg(G.hh_ena + gi), ek = __ldg(G.hh_ek + gi), el = __ldg(G.hh_el + gi);
         double g1 = hh_current(vi + kFdEps, gnabar, gkbar, gl, m, h, n, ena, ek, el);
         const double i0 = hh_current(vi, gnabar, gkbar, gl, m, h, n, ena, ek, el);
-        g1 = (g1 - i0) / kFdEps;
+        g1 = (g1 - i0) * kInvFdEps;
         r -= i0;
         dd += g1;
     }
-    for (int k = G.node_ic_off[gi]; k < G.node_ic_off[gi + 1]; ++k) {  // iclamp_templated.cu:35-45, electrode
-        const int j = G.node_ic[k];
-        const double del = G.ic_del[j], dur = G.ic_dur[j];
-        const double cur = (tmid < del + dur && tmid >= del) ? G.ic_amp[j] : 0.0;
-        double g1 = (cur - cur) / kFdEps;
-        double i0 = cur;
-        const double s = 1.e2 / G.area[gi];
-        g1 *= s;
-        i0 *= s;
-        r += i0;
-        dd -= g1;
+    const int ic1 = __ldg(G.node_ic_off + gi + 1);
+    for (int k = __ldg(G.node_ic_off + gi); k < ic1; ++k) {  // iclamp_templated.cu:35-45, electrode
+        const int j = __ldg(G.node_ic + k);
+        const double del = __ldg(G.ic_del + j), dur = __ldg(G.ic_dur + j);
+        const double cur = (tmid < del + dur && tmid >= del) ? __ldg(G.ic_amp + j) : 0.0;
+        r += cur * (1.e2 / __ldg(G.area + gi));
     }
-    dd += G.cfac * G.cm[gi];
-    const int par = G.node_parent[gi];
-    const int c0 = G.node_child_off[gi], c1 = G.node_child_off[gi + 1];
-    if (kRhs) {
-        if (par >= 0) {
-            const double dv = sv[par] - vi;
-            r -= sb[i] * dv;
-        }
-        for (int k = c0; k < c1; ++k) {
-            const int c = G.node_child[k];
-            const double dv = vi - sv[c];
-            r += sa[c] * dv;
-        }
+    dd += G.cfac * __ldg(G.cm + gi);
+    const int par = M.par[i];
+    if (par >= 0) {
+        if (kRhs) r -= sb[i] * (sv[par] - vi);
+        dd -= sb[i];
     }
-    if (par >= 0) dd -= sb[i];
-    for (int k = c0; k < c1; ++k) dd -= sa[G.node_child[k]];
+    const int c1 = M.cho[i + 1];
+    for (int k = M.cho[i]; k < c1; ++k) {
+        const int c = M.ch[k];
+        const double ac = sa[c];
+        if (kRhs) r += ac * (vi - sv[c]);
+        dd -= ac;
+    }
     r_out = r;
     d_out = dd;
 }
 
+// ------------------------------------------------------------------ init
+__global__ void init_state_kernel(DevGroup G, DevState S, double v_init) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= G.nnode) return;
+    S.v[i] = v_init;
+    double m = 0.0, h = 0.0, n = 0.0;
+    if (G.node_flags[i] & kHasHH) {  // hh INITIAL: gates at steady state (hh_templated.cu:111-122)
+        HHRates r;
+        hh_rates(v_init, G.q10, r);
+        m = r.inf[0];
+        h = r.inf[1];
+        n = r.inf[2];
+    }
+    S.m[i] = m;
+    S.h[i] = h;
+    S.n[i] = n;
+}
+
 // ------------------------------------------------------------------ forward
-__global__ void __launch_bounds__(kThreads) fwd_kernel(DevGroup G, DevState S, DevTape T, int write_tape,
-                                                        DevProbe P, double* __restrict__ trace,
-                                                        const double* __restrict__ tmid, int k0, int k1) {
+__global__ void __launch_bounds__(kThreads, 2) fwd_kernel(DevGroup G, DevState S, DevTape T, int write_tape,
+                                                           DevProbe P, double* __restrict__ trace,
+                                                           const double* __restrict__ tmid, int k0, int k1) {
     extern __shared__ double smem[];
     const int p = blockIdx.x;
-    const int tid = threadIdx.x, nt = blockDim.x;
-    const int nb = G.pack_node_off[p], n = G.pack_node_off[p + 1] - nb;
-    const int hb = G.pack_hh_off[p], nh = G.pack_hh_off[p + 1] - hb;
+    const int N = G.smem_n;
     double* sv = smem;
-    double* srhs = sv + G.smem_n;
-    double* sd = srhs + G.smem_n;
-    double* sa = sd + G.smem_n;
-    double* sb = sa + G.smem_n;
-    double* sgm = sb + G.smem_n;
-    double* sgh = sgm + G.smem_nh;
-    double* sgn = sgh + G.smem_nh;
-    for (int i = tid; i < n; i += nt) {
-        sv[i] = S.v[nb + i];
-        sa[i] = G.a[nb + i];
-        sb[i] = G.b[nb + i];
-    }
-    for (int j = tid; j < nh; j += nt) {
-        sgm[j] = S.m[hb + j];
-        sgh[j] = S.h[hb + j];
-        sgn[j] = S.n[hb + j];
+    double* srhs = sv + N;
+    double* sd = srhs + N;
+    double* sa = sd + N;
+    double* sb = sa + N;
+    double* sgm = sb + N;
+    double* sgh = sgm + N;
+    double* sgn = sgh + N;
+    Meta M;
+    Grp g;
+    if (!setup_pack(G, p, reinterpret_cast<int*>(sgn + N), M, g)) return;
+    const int pb = G.pack_node_off[p];
+    const int i0 = g.nb, i1 = g.nb + g.n;
+    for (int i = i0 + g.tl; i < i1; i += g.nt) {
+        sv[i] = S.v[pb + i];
+        sa[i] = G.a[pb + i];
+        sb[i] = G.b[pb + i];
+        sgm[i] = S.m[pb + i];
+        sgh[i] = S.h[pb + i];
+        sgn[i] = S.n[pb + i];
     }
     const int q0 = P.pack_off[p], q1 = P.pack_off[p + 1];
-    __syncthreads();
+    g.sync();
     if (k0 == 0 && trace)
-        for (int q = q0 + tid; q < q1; q += nt) trace[P.slot[q]] = sv[P.local[q]];
+        for (int q = q0 + g.tl; q < q1; q += g.nt) {
+            const int l = P.local[q];
+            if (l >= i0 && l < i1) trace[P.slot[q]] = sv[l];
+        }
     for (int k = k0; k < k1; ++k) {
         if (write_tape) {
-            const size_t row = (size_t)(k - T.k_base);
-            double* tv = T.v + row * (size_t)G.nnode + nb;
-            for (int i = tid; i < n; i += nt) tv[i] = sv[i];
-            const size_t ho = row * (size_t)G.nhh + hb;
-            for (int j = tid; j < nh; j += nt) {
-                T.m[ho + j] = sgm[j];
-                T.h[ho + j] = sgh[j];
-                T.n[ho + j] = sgn[j];
+            const size_t off = (size_t)(k - T.k_base) * (size_t)G.nnode + pb;
+            for (int i = i0 + g.tl; i < i1; i += g.nt) {
+                T.v[off + i] = sv[i];
+                T.m[off + i] = sgm[i];
+                T.h[off + i] = sgh[i];
+                T.n[off + i] = sgn[i];
             }
         }
         const double tm = tmid[k];
         // A: assembly
-        for (int i = tid; i < n; i += nt) {
-            const int jh = G.node_hh[nb + i];
-            double gm = 0.0, gh = 0.0, gn = 0.0;
-            if (jh >= 0) {
-                gm = sgm[jh];
-                gh = sgh[jh];
-                gn = sgn[jh];
-            }
+        for (int i = i0 + g.tl; i < i1; i += g.nt) {
             double r, dd;
-            assemble<true>(G, nb, hb, i, sv, sa, sb, jh, gm, gh, gn, tm, r, dd);
+            assemble<true>(G, M, pb, i, M.flag[i], sv, sa, sb, sgm[i], sgh[i], sgn[i], tm, r, dd);
             srhs[i] = r;
             sd[i] = dd;
         }
-        __syncthreads();
+        g.sync();
         // B: Hines solve (rhs := dv)
-        hines_smem(G, p, sa, sb, sd, srhs);
+        hines_cell<false>(M, g, sa, sb, sd, srhs);
         // C: update + states
-        for (int i = tid; i < n; i += nt) {
+        for (int i = i0 + g.tl; i < i1; i += g.nt) {
             const double vn = sv[i] + srhs[i];
             sv[i] = vn;
-            const int jh = G.node_hh[nb + i];
-            if (jh >= 0) {
+            if (M.flag[i] & kHasHH) {
                 HHRates r;
                 hh_rates(vn, G.q10, r);
-                sgm[jh] = gate_step(sgm[jh], r.minf, r.mtau, G.dt);
-                sgh[jh] = gate_step(sgh[jh], r.hinf, r.htau, G.dt);
-                sgn[jh] = gate_step(sgn[jh], r.ninf, r.ntau, G.dt);
+                sgm[i] = gate_step(sgm[i], r.inf[0], r.k[0], G.dt);
+                sgh[i] = gate_step(sgh[i], r.inf[1], r.k[1], G.dt);
+                sgn[i] = gate_step(sgn[i], r.inf[2], r.k[2], G.dt);
             }
         }
-        __syncthreads();
+        g.sync();
         if (trace)
-            for (int q = q0 + tid; q < q1; q += nt) trace[(size_t)(k + 1) * P.nprobe + P.slot[q]] = sv[P.local[q]];
+            for (int q = q0 + g.tl; q < q1; q += g.nt) {
+                const int l = P.local[q];
+                if (l >= i0 && l < i1) trace[(size_t)(k + 1) * P.nprobe + P.slot[q]] = sv[l];
+            }
     }
     if (write_tape) {
-        double* tv = T.v + (size_t)(k1 - T.k_base) * (size_t)G.nnode + nb;
-        for (int i = tid; i < n; i += nt) tv[i] = sv[i];
+        const size_t off = (size_t)(k1 - T.k_base) * (size_t)G.nnode + pb;
+        for (int i = i0 + g.tl; i < i1; i += g.nt) T.v[off + i] = sv[i];
     }
-    for (int i = tid; i < n; i += nt) S.v[nb + i] = sv[i];
-    for (int j = tid; j < nh; j += nt) {
-        S.m[hb + j] = sgm[j];
-        S.h[hb + j] = sgh[j];
-        S.n[hb + j] = sgn[j];
+    for (int i = i0 + g.tl; i < i1; i += g.nt) {
+        S.v[pb + i] = sv[i];
+        S.m[pb + i] = sgm[i];
+        S.h[pb + i] = sgh[i];
+        S.n[pb + i] = sgn[i];
     }
 }
 
 // ------------------------------------------------------------------ backward
 // Reverse sweep over steps [k_lo, k_hi).  Per step k, with lv = dL/dv_{k+1}
 // and lm/lh/ln = dL/d(gates_{k+1}):
-//   S  gates_{k+1} = E*gates_k + (1-E)*inf(v_{k+1}):  mu = lv + sum lg*dgate'/dv',
-//      lg *= E;
+//   S  gates_{k+1} = E*gates_k + (1-E)*inf(v_{k+1}), E = exp(-dt k(v_{k+1})):
+//      mu = lv + sum lg*dgate'/dv', lg *= E;
 //   A  recompute the diagonal d_k (FD conductances at v_k, gates_k);
 //   B  w = M_k^{-T} mu (Hines with a and b swapped);
 //   V  lambda_d = -w*dv; VJPs of rhs_k and d_k into lv (dL/dv_k), the gate
-//      adjoints and the per-instance parameter gradients.
-__global__ void __launch_bounds__(kThreads) bwd_kernel(DevGroup G, DevTape T, DevAdj A, DevGrad GR, DevProbe P,
-                                                        const double* __restrict__ dLdv,
-                                                        const double* __restrict__ tmid, int k_hi, int k_lo) {
+//      adjoints and the per-node parameter gradients.
+__global__ void __launch_bounds__(kThreads, 2) bwd_kernel(DevGroup G, DevTape T, DevAdj Ad, DevGrad GR, DevProbe P,
+                                                           const double* __restrict__ dLdv,
+                                                           const double* __restrict__ tmid, int k_hi, int k_lo) {
     extern __shared__ double smem[];
     const int p = blockIdx.x;
-    const int tid = threadIdx.x, nt = blockDim.x;
-    const int nb = G.pack_node_off[p], n = G.pack_node_off[p + 1] - nb;
-    const int hb = G.pack_hh_off[p], nh = G.pack_hh_off[p + 1] - hb;
+    const int N = G.smem_n;
     double* slv = smem;
-    double* sw = slv + G.smem_n;
-    double* sd = sw + G.smem_n;
-    double* svk = sd + G.smem_n;
-    double* svk1 = svk + G.smem_n;
-    double* sa = svk1 + G.smem_n;
-    double* sb = sa + G.smem_n;
-    double* slm = sb + G.smem_n;
-    double* slh = slm + G.smem_nh;
-    double* sln = slh + G.smem_nh;
+    double* sw = slv + N;
+    double* sd = sw + N;
+    double* sa = sd + N;
+    double* sb = sa + N;
+    double* svk = sb + N;
+    double* svk1 = svk + N;
+    double* slm = svk1 + N;
+    double* slh = slm + N;
+    double* sln = slh + N;
+    Meta M;
+    Grp g;
+    if (!setup_pack(G, p, reinterpret_cast<int*>(sln + N), M, g)) return;
+    const int pb = G.pack_node_off[p];
+    const int i0 = g.nb, i1 = g.nb + g.n;
     const double dt = G.dt, q10 = G.q10;
-    for (int i = tid; i < n; i += nt) {
-        slv[i] = A.lv[nb + i];
-        sa[i] = G.a[nb + i];
-        sb[i] = G.b[nb + i];
-        svk1[i] = T.v[(size_t)(k_hi - T.k_base) * (size_t)G.nnode + nb + i];
-    }
-    for (int j = tid; j < nh; j += nt) {
-        slm[j] = A.lm[hb + j];
-        slh[j] = A.lh[hb + j];
-        sln[j] = A.ln[hb + j];
+    for (int i = i0 + g.tl; i < i1; i += g.nt) {
+        slv[i] = Ad.lv[pb + i];
+        sa[i] = G.a[pb + i];
+        sb[i] = G.b[pb + i];
+        slm[i] = Ad.lm[pb + i];
+        slh[i] = Ad.lh[pb + i];
+        sln[i] = Ad.ln[pb + i];
+        svk1[i] = T.v[(size_t)(k_hi - T.k_base) * (size_t)G.nnode + pb + i];
     }
     const int q0 = P.pack_off[p], q1 = P.pack_off[p + 1];
-    __syncthreads();
+    g.sync();
     for (int k = k_hi - 1; k >= k_lo; --k) {
-        const size_t row = (size_t)(k - T.k_base);
-        const double* tv = T.v + row * (size_t)G.nnode + nb;
-        const double* tgm = T.m + row * (size_t)G.nhh + hb;
-        const double* tgh = T.h + row * (size_t)G.nhh + hb;
-        const double* tgn = T.n + row * (size_t)G.nhh + hb;
-        for (int i = tid; i < n; i += nt) svk[i] = tv[i];
-        if (tid == 0)
-            for (int q = q0; q < q1; ++q) slv[P.local[q]] += dLdv[(size_t)(k + 1) * P.nprobe + P.slot[q]];
-        __syncthreads();
+        const size_t off = (size_t)(k - T.k_base) * (size_t)G.nnode + pb;
+        for (int i = i0 + g.tl; i < i1; i += g.nt) svk[i] = T.v[off + i];
+        if (g.tl == 0)
+            for (int q = q0; q < q1; ++q) {
+                const int l = P.local[q];
+                if (l >= i0 && l < i1) slv[l] += dLdv[(size_t)(k + 1) * P.nprobe + P.slot[q]];
+            }
+        g.sync();
         const double tm = tmid[k];
         // S + A
-        for (int i = tid; i < n; i += nt) {
+        for (int i = i0 + g.tl; i < i1; i += g.nt) {
             double mu = slv[i];
-            const int jh = G.node_hh[nb + i];
+            const int fl = M.flag[i];
             double gm = 0.0, gh = 0.0, gn = 0.0;
-            if (jh >= 0) {
-                gm = tgm[jh];
-                gh = tgh[jh];
-                gn = tgn[jh];
+            if (fl & kHasHH) {
+                gm = T.m[off + i];
+                gh = T.h[off + i];
+                gn = T.n[off + i];
                 HHRatesD R;
                 hh_rates_d(svk1[i], q10, R);
                 const double x[3] = {gm, gh, gn};
-                double lam[3] = {slm[jh], slh[jh], sln[jh]};
+                double lam[3] = {slm[i], slh[i], sln[i]};
 #pragma unroll
                 for (int q = 0; q < 3; ++q) {
-                    const double E = exp(dt * (-1.0 / R.tau[q]));
+                    const double E = exp(-dt * R.k[q]);
                     const double dnew = (1.0 - E) * R.dinf[q] + (R.inf[q] - x[q]) * E * dt * q10 * R.ds[q];
                     mu += lam[q] * dnew;
                     lam[q] *= E;
                 }
-                slm[jh] = lam[0];
-                slh[jh] = lam[1];
-                sln[jh] = lam[2];
+                slm[i] = lam[0];
+                slh[i] = lam[1];
+                sln[i] = lam[2];
             }
             double r, dd;
-            assemble<false>(G, nb, hb, i, svk, sa, sb, jh, gm, gh, gn, tm, r, dd);
+            assemble<false>(G, M, pb, i, fl, svk, sa, sb, gm, gh, gn, tm, r, dd);
             sd[i] = dd;
             sw[i] = mu;
             slv[i] = mu;
         }
-        __syncthreads();
+        g.sync();
         // B: w = M^{-T} mu
-        hines_smem(G, p, sb, sa, sd, sw);
+        hines_cell<true>(M, g, sa, sb, sd, sw);
         // V
-        for (int i = tid; i < n; i += nt) {
-            const int gi = nb + i;
+        for (int i = i0 + g.tl; i < i1; i += g.nt) {
+            const int gi = pb + i;
+            const int fl = M.flag[i];
             const double w = sw[i];
             const double vk = svk[i];
             const double ld = -w * (svk1[i] - vk);
             double lvn = slv[i];
-            const int jp = G.node_pas[gi];
-            if (jp >= 0) {
-                const double g = G.pas_g[jp];
-                GR.pas_g[jp] += ld - w * (vk - G.pas_e[jp]);
-                GR.pas_e[jp] += w * g;
-                lvn -= w * g;
+            if (fl & kHasPas) {
+                const double gp = __ldg(G.pas_g + gi);
+                GR.pas_g[gi] += ld - w * (vk - __ldg(G.pas_e + gi));
+                GR.pas_e[gi] += w * gp;
+                lvn -= w * gp;
             }
-            const int jh = G.node_hh[gi];
-            if (jh >= 0) {
-                const int gj = hb + jh;
-                const double m = tgm[jh], h = tgh[jh], nn = tgn[jh];
-                const double gnabar = G.hh_gnabar[gj], gkbar = G.hh_gkbar[gj], gl = G.hh_gl[gj];
-                const double t_na = ld - w * (vk - G.hh_ena[gj]);
-                const double t_k = ld - w * (vk - G.hh_ek[gj]);
-                const double t_l = ld - w * (vk - G.hh_el[gj]);
+            if (fl & kHasHH) {
+                const double m = T.m[off + i], h = T.h[off + i], nn = T.n[off + i];
+                const double gnabar = __ldg(G.hh_gnabar + gi), gkbar = __ldg(G.hh_gkbar + gi), gl = __ldg(G.hh_gl + gi);
+                const double t_na = ld - w * (vk - __ldg(G.hh_ena + gi));
+                const double t_k = ld - w * (vk - __ldg(G.hh_ek + gi));
+                const double t_l = ld - w * (vk - __ldg(G.hh_el + gi));
                 const double m2h = m * m * h, n3 = nn * nn * nn;
-                GR.hh_gnabar[gj] += m2h * m * t_na;
-                GR.hh_gkbar[gj] += n3 * nn * t_k;
-                GR.hh_gl[gj] += t_l;
-                GR.hh_el[gj] += w * gl;
-                slm[jh] += 3.0 * gnabar * m2h * t_na;
-                slh[jh] += gnabar * m * m * m * t_na;
-                sln[jh] += 4.0 * gkbar * n3 * t_k;
+                GR.hh_gnabar[gi] += m2h * m * t_na;
+                GR.hh_gkbar[gi] += n3 * nn * t_k;
+                GR.hh_gl[gi] += t_l;
+                GR.hh_el[gi] += w * gl;
+                slm[i] += 3.0 * gnabar * m2h * t_na;
+                slh[i] += gnabar * m * m * m * t_na;
+                sln[i] += 4.0 * gkbar * n3 * t_k;
                 lvn -= w * (gnabar * m2h * m + gkbar * n3 * nn + gl);
             }
-            for (int k2 = G.node_ic_off[gi]; k2 < G.node_ic_off[gi + 1]; ++k2) {
-                const int j = G.node_ic[k2];
-                const double del = G.ic_del[j], dur = G.ic_dur[j];
-                if (tm < del + dur && tm >= del) GR.ic_amp[j] += w * (1.e2 / G.area[gi]);
+            const int ic1 = __ldg(G.node_ic_off + gi + 1);
+            for (int k2 = __ldg(G.node_ic_off + gi); k2 < ic1; ++k2) {
+                const int j = __ldg(G.node_ic + k2);
+                const double del = __ldg(G.ic_del + j), dur = __ldg(G.ic_dur + j);
+                if (tm < del + dur && tm >= del) GR.ic_amp[j] += w * (1.e2 / __ldg(G.area + gi));
             }
             GR.cm[gi] += ld * G.cfac;
-            const int par = G.node_parent[gi];
+            const int par = M.par[i];
             if (par >= 0) lvn += sb[i] * w - sa[i] * sw[par];
-            for (int k2 = G.node_child_off[gi]; k2 < G.node_child_off[gi + 1]; ++k2) {
-                const int c = G.node_child[k2];
+            const int c1 = M.cho[i + 1];
+            for (int k2 = M.cho[i]; k2 < c1; ++k2) {
+                const int c = M.ch[k2];
                 lvn += sa[c] * w - sb[c] * sw[c];
             }
             slv[i] = lvn;
@@ -376,13 +551,13 @@ __global__ void __launch_bounds__(kThreads) bwd_kernel(DevGroup G, DevTape T, De
         double* tmp = svk1;
         svk1 = svk;
         svk = tmp;
-        __syncthreads();
+        g.sync();
     }
-    for (int i = tid; i < n; i += nt) A.lv[nb + i] = slv[i];
-    for (int j = tid; j < nh; j += nt) {
-        A.lm[hb + j] = slm[j];
-        A.lh[hb + j] = slh[j];
-        A.ln[hb + j] = sln[j];
+    for (int i = i0 + g.tl; i < i1; i += g.nt) {
+        Ad.lv[pb + i] = slv[i];
+        Ad.lm[pb + i] = slm[i];
+        Ad.lh[pb + i] = slh[i];
+        Ad.ln[pb + i] = sln[i];
     }
 }
 
@@ -411,8 +586,11 @@ __global__ void reduce_cols_kernel(const double* __restrict__ grad, const int* _
 }
 
 // ------------------------------------------------------------------ launchers
-size_t fwd_smem_bytes(const DevGroup& G) { return sizeof(double) * (5 * (size_t)G.smem_n + 3 * (size_t)G.smem_nh); }
-size_t bwd_smem_bytes(const DevGroup& G) { return sizeof(double) * (7 * (size_t)G.smem_n + 3 * (size_t)G.smem_nh); }
+static size_t meta_bytes(const DevGroup& G) {
+    return sizeof(int) * (3 * (size_t)G.smem_n + 1 + G.smem_nch + 4 * (size_t)G.smem_br + 1 + G.smem_bch + G.smem_lvl);
+}
+size_t fwd_smem_bytes(const DevGroup& G) { return sizeof(double) * 8 * (size_t)G.smem_n + meta_bytes(G); }
+size_t bwd_smem_bytes(const DevGroup& G) { return sizeof(double) * 10 * (size_t)G.smem_n + meta_bytes(G); }
 
 cudaError_t configure_kernels(size_t smem_fwd, size_t smem_bwd) {
     cudaError_t e = cudaFuncSetAttribute(fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_fwd);
@@ -421,8 +599,7 @@ cudaError_t configure_kernels(size_t smem_fwd, size_t smem_bwd) {
 }
 
 cudaError_t launch_init(const DevGroup& G, const DevState& S, double v_init, cudaStream_t st) {
-    int n = G.nnode > G.nhh ? G.nnode : G.nhh;
-    init_state_kernel<<<(n + 255) / 256, 256, 0, st>>>(G, S, v_init);
+    init_state_kernel<<<(G.nnode + 255) / 256, 256, 0, st>>>(G, S, v_init);
     return cudaGetLastError();
 }
 

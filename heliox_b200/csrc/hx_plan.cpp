@@ -57,7 +57,7 @@ std::string validate(const hx_group_desc& g) {
 
 }  // namespace
 
-std::string build_plan(const hx_group_desc& g, int nodes_per_pack, Plan& P) {
+std::string build_plan(const hx_group_desc& g, int nodes_per_warp, int max_pack_nodes, Plan& P) {
     std::string err = validate(g);
     if (!err.empty()) return err;
     P = Plan();
@@ -86,7 +86,8 @@ std::string build_plan(const hx_group_desc& g, int nodes_per_pack, Plan& P) {
     std::vector<int> cell_size(ncell, 0);
     for (int i = 0; i < n; i++) cell_size[cell[i]]++;
 
-    // branch decomposition per cell (BFS over branches from the root)
+    // branch decomposition per cell (BFS over branches from the root), then
+    // branches sorted by (level, head reference index)
     std::vector<std::vector<Branch>> cbr(ncell);
     for (int c = 0; c < ncell; c++) {
         std::vector<Branch>& B = cbr[c];
@@ -110,52 +111,81 @@ std::string build_plan(const hx_group_desc& g, int nodes_per_pack, Plan& P) {
             int me = (int)B.size() - 1;
             for (int k = child_off[cur]; k < child_off[cur + 1]; k++) q.push({child[k], me});
         }
+        std::stable_sort(B.begin(), B.end(), [](const Branch& x, const Branch& y) {
+            if (x.level != y.level) return x.level < y.level;
+            return x.head_ref < y.head_ref;
+        });
     }
 
-    // pack cells: LPT (largest first onto the least-loaded pack)
-    long long total = n;
-    int target = nodes_per_pack > 0 ? nodes_per_pack : 1024;
-    int maxcell = *std::max_element(cell_size.begin(), cell_size.end());
-    if (target < maxcell) target = maxcell;
-    long long npack = (total + target - 1) / target;
-    if (npack < 1) npack = 1;
-    if (npack > ncell) npack = ncell;
-    if (npack >= 148) npack = ((npack + 147) / 148) * 148;
-    if (npack > ncell) npack = ncell;
-    P.npack = (int)npack;
+    // warps per cell and first-fit-decreasing packing into CTAs of kWarpsPerCta
+    // warps with a node capacity (shared memory)
+    const int npw = nodes_per_warp > 0 ? nodes_per_warp : 144;
+    const int maxcell = *std::max_element(cell_size.begin(), cell_size.end());
+    int cap = npw * kWarpsPerCta;
+    if (max_pack_nodes > 0) {
+        if (maxcell > max_pack_nodes)
+            return "a cell of " + std::to_string(maxcell) + " nodes exceeds the per-CTA capacity of " +
+                   std::to_string(max_pack_nodes) + " nodes";
+        cap = std::min(cap, max_pack_nodes);
+    }
+    cap = std::max(cap, maxcell);
+    std::vector<int> wc(ncell);
+    for (int c = 0; c < ncell; c++) wc[c] = std::min(kWarpsPerCta, std::max(1, (cell_size[c] + npw - 1) / npw));
     std::vector<int> order(ncell);
     std::iota(order.begin(), order.end(), 0);
     std::stable_sort(order.begin(), order.end(), [&](int x, int y) { return cell_size[x] > cell_size[y]; });
-    std::vector<std::vector<int>> pack_cells(npack);
-    {
-        using E = std::pair<long long, int>;  // (load, pack)
-        std::priority_queue<E, std::vector<E>, std::greater<E>> pq;
-        for (int p = 0; p < npack; p++) pq.push({0, p});
-        for (int c : order) {
-            auto [ld, p] = pq.top();
-            pq.pop();
-            pack_cells[p].push_back(c);
-            pq.push({ld + cell_size[c], p});
+    std::vector<std::vector<int>> bins;
+    std::vector<int> bin_w, bin_n;
+    for (int c : order) {
+        int b = -1;
+        for (int k = 0; k < (int)bins.size(); k++)
+            if (bin_w[k] + wc[c] <= kWarpsPerCta && bin_n[k] + cell_size[c] <= cap) {
+                b = k;
+                break;
+            }
+        if (b < 0) {
+            bins.push_back({});
+            bin_w.push_back(0);
+            bin_n.push_back(0);
+            b = (int)bins.size() - 1;
         }
-        for (auto& v : pack_cells) std::sort(v.begin(), v.end());
+        bins[b].push_back(c);
+        bin_w[b] += wc[c];
+        bin_n[b] += cell_size[c];
     }
+    // hand the spare warps of each CTA to its cells with the most nodes per warp
+    for (size_t b = 0; b < bins.size(); b++) {
+        int spare = kWarpsPerCta - bin_w[b];
+        while (spare > 0) {
+            int best = -1;
+            double bestv = -1;
+            for (int c : bins[b]) {
+                double v = (double)cell_size[c] / wc[c];
+                if (wc[c] < kWarpsPerCta && v > bestv) {
+                    bestv = v;
+                    best = c;
+                }
+            }
+            if (best < 0) break;
+            wc[best]++;
+            spare--;
+        }
+        std::sort(bins[b].begin(), bins[b].end());
+    }
+    const int npack = (int)bins.size();
+    P.npack = npack;
 
     // layout
     P.pack_node_off.assign(npack + 1, 0);
-    P.pack_hh_off.assign(npack + 1, 0);
+    P.pack_slot_off.assign(npack + 1, 0);
     P.pack_br_off.assign(npack + 1, 0);
-    P.pack_lvl_off.assign(npack + 1, 0);
-    P.pack_nlev.assign(npack, 0);
+    P.pack_bch_off.assign(npack + 1, 0);
+    P.pack_nch_off.assign(npack + 1, 0);
     P.gpu2ref.resize(n);
     P.ref2gpu.assign(n, -1);
     P.node_parent.resize(n);
     P.node_cell.resize(n);
     P.br_child_off.push_back(0);
-
-    // density instance lookup by reference node
-    std::vector<int> hh_of(n, -1), pas_of(n, -1);
-    for (int j = 0; j < g.nhh; j++) hh_of[g.hh_node[j]] = j;
-    for (int j = 0; j < g.npas; j++) pas_of[g.pas_node[j]] = j;
     std::vector<int> ic_cnt(n, 0);
     for (int j = 0; j < g.nic; j++) ic_cnt[g.ic_node[j]]++;
     std::vector<int> ic_first(n + 1, 0);
@@ -164,112 +194,107 @@ std::string build_plan(const hx_group_desc& g, int nodes_per_pack, Plan& P) {
     int gpos = 0;
     long long sum_nodes = 0;
     for (int p = 0; p < npack; p++) {
-        // collect branches of the pack's cells, ordered by (level, cell, head)
-        struct BRef {
-            int c, b;
-        };
-        std::vector<BRef> brs;
-        for (int c : pack_cells[p])
-            for (int b = 0; b < (int)cbr[c].size(); b++) brs.push_back({c, b});
-        std::stable_sort(brs.begin(), brs.end(), [&](const BRef& x, const BRef& y) {
-            const Branch& X = cbr[x.c][x.b];
-            const Branch& Y = cbr[y.c][y.b];
-            if (X.level != Y.level) return X.level < Y.level;
-            if (x.c != y.c) return x.c < y.c;
-            return X.head_ref < Y.head_ref;
-        });
         const int base = gpos;
-        std::vector<int> ref2loc_local;  // filled via P.ref2gpu
-        int nlev = 0;
-        for (auto& r : brs) nlev = std::max(nlev, cbr[r.c][r.b].level + 1);
-        P.pack_nlev[p] = nlev;
-        // level offsets
-        std::vector<int> lvl_off(nlev + 1, 0);
-        for (auto& r : brs) lvl_off[cbr[r.c][r.b].level + 1]++;
-        for (int L = 0; L < nlev; L++) lvl_off[L + 1] += lvl_off[L];
-        for (int L = 0; L <= nlev; L++) P.level_br_off.push_back(lvl_off[L]);
-        P.pack_lvl_off[p + 1] = P.pack_lvl_off[p] + nlev + 1;
-        // assign node positions
-        for (auto& r : brs) {
-            const Branch& B = cbr[r.c][r.b];
-            for (int ref : B.nodes) {
-                P.gpu2ref[gpos] = ref;
-                P.ref2gpu[ref] = gpos;
-                P.node_cell[gpos] = r.c;
-                gpos++;
-            }
+        int wpos = 0, bar = 1, brl = 0;
+        int pack_levels = 0, crit = 0;
+        for (int c : bins[p]) {
+            const std::vector<Branch>& B = cbr[c];
+            P.cs_cell.push_back(c);
+            P.cs_node0.push_back(gpos - base);
+            P.cs_nnode.push_back(cell_size[c]);
+            P.cs_warp0.push_back(wpos);
+            P.cs_nwarp.push_back(wc[c]);
+            P.cs_bar.push_back(wc[c] > 1 ? bar++ : 0);
+            wpos += wc[c];
+            int nlev = B.back().level + 1;
+            P.cs_lvl_off.push_back((int)P.level_br_off.size());
+            P.cs_nlev.push_back(nlev);
+            std::vector<int> lvl(nlev + 1, 0);
+            for (const Branch& br : B) lvl[br.level + 1]++;
+            for (int L = 0; L < nlev; L++) lvl[L + 1] += lvl[L];
+            for (int L = 0; L <= nlev; L++) P.level_br_off.push_back(brl + lvl[L]);
+            brl += (int)B.size();
+            pack_levels = std::max(pack_levels, nlev);
+            for (const Branch& br : B)
+                for (int ref : br.nodes) {
+                    P.gpu2ref[gpos] = ref;
+                    P.ref2gpu[ref] = gpos;
+                    P.node_cell[gpos] = c;
+                    gpos++;
+                }
         }
+        // branches of the pack (cell by cell, already level-sorted)
+        for (int c : bins[p])
+            for (const Branch& br : cbr[c]) {
+                P.br_head.push_back(P.ref2gpu[br.head_ref] - base);
+                P.br_end.push_back(P.ref2gpu[br.end_ref] - base);
+                int hp = g.parent[br.head_ref];
+                P.br_parent.push_back(hp < 0 ? -1 : P.ref2gpu[hp] - base);
+                int e = br.end_ref;
+                for (int k = child_off[e + 1] - 1; k >= child_off[e]; k--)
+                    P.br_child.push_back(P.ref2gpu[child[k]] - base);
+                P.br_child_off.push_back((int)P.br_child.size());
+            }
         const int pn = gpos - base;
         sum_nodes += pn;
-        // branches
-        int crit = 0;
-        std::vector<int> path_len(brs.size(), 0);
-        for (size_t bi = 0; bi < brs.size(); bi++) {
-            const Branch& B = cbr[brs[bi].c][brs[bi].b];
-            P.br_head.push_back(P.ref2gpu[B.head_ref] - base);
-            P.br_end.push_back(P.ref2gpu[B.end_ref] - base);
-            int hp = g.parent[B.head_ref];
-            P.br_parent.push_back(hp < 0 ? -1 : P.ref2gpu[hp] - base);
-            // child heads of the branch end, descending reference index
-            int e = B.end_ref;
-            for (int k = child_off[e + 1] - 1; k >= child_off[e]; k--) P.br_child.push_back(P.ref2gpu[child[k]] - base);
-            P.br_child_off.push_back((int)P.br_child.size());
-        }
-        // critical path (nodes on the longest root->leaf chain)
         {
             std::vector<int> depth(pn, 0);
             for (int l = 0; l < pn; l++) {
-                int ref = P.gpu2ref[base + l];
-                int pr = g.parent[ref];
+                int pr = g.parent[P.gpu2ref[base + l]];
                 depth[l] = pr < 0 ? 1 : depth[P.ref2gpu[pr] - base] + 1;
                 crit = std::max(crit, depth[l]);
             }
         }
-        P.pack_br_off[p + 1] = P.pack_br_off[p] + (int)brs.size();
+        P.pack_slot_off[p + 1] = (int)P.cs_cell.size();
+        P.pack_br_off[p + 1] = P.pack_br_off[p] + brl;
+        P.pack_bch_off[p + 1] = (int)P.br_child.size();
         P.pack_node_off[p + 1] = gpos;
-        P.max_pack_nodes = std::max(P.max_pack_nodes, pn);
-        P.max_levels = std::max(P.max_levels, nlev);
-        P.max_crit = std::max(P.max_crit, crit);
-    }
-    P.imbalance = (double)P.max_pack_nodes / ((double)sum_nodes / (double)npack);
-
-    // node parent / children in pack-local ids
-    P.node_child_off.assign(n + 1, 0);
-    for (int p = 0; p < npack; p++) {
-        const int base = P.pack_node_off[p];
-        for (int gi = base; gi < P.pack_node_off[p + 1]; gi++) {
+        // node parent / children (pack-local)
+        for (int gi = base; gi < gpos; gi++) {
             int ref = P.gpu2ref[gi];
             int pr = g.parent[ref];
             P.node_parent[gi] = pr < 0 ? -1 : P.ref2gpu[pr] - base;
             for (int k = child_off[ref]; k < child_off[ref + 1]; k++) P.node_child.push_back(P.ref2gpu[child[k]] - base);
-            P.node_child_off[gi + 1] = (int)P.node_child.size();
+        }
+        P.pack_nch_off[p + 1] = (int)P.node_child.size();
+        P.max_pack_nodes = std::max(P.max_pack_nodes, pn);
+        P.max_levels = std::max(P.max_levels, pack_levels);
+        P.max_crit = std::max(P.max_crit, crit);
+        P.max_pack_branches = std::max(P.max_pack_branches, brl);
+        P.max_pack_bch = std::max(P.max_pack_bch, P.pack_bch_off[p + 1] - P.pack_bch_off[p]);
+        P.max_pack_nch = std::max(P.max_pack_nch, P.pack_nch_off[p + 1] - P.pack_nch_off[p]);
+    }
+    P.imbalance = (double)P.max_pack_nodes / ((double)sum_nodes / (double)npack);
+    P.node_child_off.assign(n + 1, 0);
+    {
+        int k = 0;
+        for (int gi = 0; gi < n; gi++) {
+            k += nchild[P.gpu2ref[gi]];
+            P.node_child_off[gi + 1] = k;
         }
     }
 
-    // mechanism instances in GPU order
+    // mechanism instances
+    std::vector<int> hh_of(n, -1), pas_of(n, -1);
+    for (int j = 0; j < g.nhh; j++) hh_of[g.hh_node[j]] = j;
+    for (int j = 0; j < g.npas; j++) pas_of[g.pas_node[j]] = j;
     P.node_hh.assign(n, -1);
     P.node_pas.assign(n, -1);
     P.node_ic_off.assign(n + 1, 0);
     for (int p = 0; p < npack; p++) {
-        int hh_local = 0;
+        int hh_cnt = 0;
         for (int gi = P.pack_node_off[p]; gi < P.pack_node_off[p + 1]; gi++) {
             int ref = P.gpu2ref[gi];
-            if (hh_of[ref] >= 0) {
-                P.node_hh[gi] = hh_local++;
-                P.hh_gpu2ref.push_back(hh_of[ref]);
-            }
-            if (pas_of[ref] >= 0) {
-                P.node_pas[gi] = (int)P.pas_gpu2ref.size();
-                P.pas_gpu2ref.push_back(pas_of[ref]);
-            }
+            P.node_hh[gi] = hh_of[ref];
+            P.node_pas[gi] = pas_of[ref];
+            hh_cnt += hh_of[ref] >= 0;
             for (int k = ic_first[ref]; k < ic_first[ref + 1]; k++) {
                 P.node_ic.push_back((int)P.ic_gpu2ref.size());
                 P.ic_gpu2ref.push_back(k);
             }
             P.node_ic_off[gi + 1] = (int)P.node_ic.size();
         }
-        P.pack_hh_off[p + 1] = P.pack_hh_off[p] + hh_local;
-        P.max_pack_hh = std::max(P.max_pack_hh, hh_local);
+        P.max_pack_hh = std::max(P.max_pack_hh, hh_cnt);
     }
     if (P.br_child.empty()) P.br_child.push_back(0);
     if (P.node_child.empty()) P.node_child.push_back(0);
@@ -277,53 +302,117 @@ std::string build_plan(const hx_group_desc& g, int nodes_per_pack, Plan& P) {
     return "";
 }
 
-void planned_solve_cpu(const Plan& P, const double* a, const double* b, double* d, double* rhs, bool transposed) {
-    const double* A = transposed ? b : a;  // factor numerator (eliminates child into parent)
-    const double* U = transposed ? a : b;  // coupling to the parent
+// Replays the schedule: per pack, per cell slot, levels deepest-first then root-first.
+template <class Tri, class Back>
+static void walk_schedule(const Plan& P, Tri tri, Back back) {
     for (int p = 0; p < P.npack; p++) {
         const int base = P.pack_node_off[p];
         const int bbase = P.pack_br_off[p];
-        const int* lo = &P.level_br_off[P.pack_lvl_off[p]];
-        const int nlev = P.pack_nlev[p];
-        double* dd = d + base;
-        double* rr = rhs + base;
-        const double* AA = A + base;
-        const double* UU = U + base;
-        for (int L = nlev - 1; L >= 0; L--) {
-            for (int br = lo[L]; br < lo[L + 1]; br++) {
-                const int gb = bbase + br;
-                const int h = P.br_head[gb], e = P.br_end[gb];
-                for (int k = P.br_child_off[gb]; k < P.br_child_off[gb + 1]; k++) {
-                    const int c = P.br_child[k];
-                    double f = AA[c] / dd[c];
-                    dd[e] -= f * UU[c];
-                    rr[e] -= f * rr[c];
-                }
-                for (int j = e; j > h; j--) {
-                    double f = AA[j] / dd[j];
-                    dd[j - 1] -= f * UU[j];
-                    rr[j - 1] -= f * rr[j];
-                }
-            }
-        }
-        for (int L = 0; L < nlev; L++) {
-            for (int br = lo[L]; br < lo[L + 1]; br++) {
-                const int gb = bbase + br;
-                const int h = P.br_head[gb], e = P.br_end[gb];
-                const int par = P.br_parent[gb];
-                if (par < 0) {
-                    rr[h] /= dd[h];
-                } else {
-                    rr[h] -= UU[h] * rr[par];
-                    rr[h] /= dd[h];
-                }
-                for (int j = h + 1; j <= e; j++) {
-                    rr[j] -= UU[j] * rr[j - 1];
-                    rr[j] /= dd[j];
-                }
-            }
+        for (int s = P.pack_slot_off[p]; s < P.pack_slot_off[p + 1]; s++) {
+            const int* lo = &P.level_br_off[P.cs_lvl_off[s]];
+            const int nlev = P.cs_nlev[s];
+            for (int L = nlev - 1; L >= 0; L--)
+                for (int br = lo[L]; br < lo[L + 1]; br++) tri(base, bbase + br);
+            for (int L = 0; L < nlev; L++)
+                for (int br = lo[L]; br < lo[L + 1]; br++) back(base, bbase + br);
         }
     }
+}
+
+void planned_solve_cpu(const Plan& P, const double* a, const double* b, double* d, double* rhs, bool transposed) {
+    const double* A = transposed ? b : a;  // eliminates a child into its parent
+    const double* U = transposed ? a : b;  // couples a node to its parent
+    walk_schedule(
+        P,
+        [&](int base, int gb) {
+            double* dd = d + base;
+            double* rr = rhs + base;
+            const double* AA = A + base;
+            const double* UU = U + base;
+            const int h = P.br_head[gb], e = P.br_end[gb];
+            for (int k = P.br_child_off[gb]; k < P.br_child_off[gb + 1]; k++) {
+                const int c = P.br_child[k];
+                double f = AA[c] / dd[c];
+                dd[e] -= f * UU[c];
+                rr[e] -= f * rr[c];
+            }
+            for (int j = e; j > h; j--) {
+                double f = AA[j] / dd[j];
+                dd[j - 1] -= f * UU[j];
+                rr[j - 1] -= f * rr[j];
+            }
+        },
+        [&](int base, int gb) {
+            double* dd = d + base;
+            double* rr = rhs + base;
+            const double* UU = U + base;
+            const int h = P.br_head[gb], e = P.br_end[gb];
+            const int par = P.br_parent[gb];
+            if (par < 0) {
+                rr[h] /= dd[h];
+            } else {
+                rr[h] -= UU[h] * rr[par];
+                rr[h] /= dd[h];
+            }
+            for (int j = h + 1; j <= e; j++) {
+                rr[j] -= UU[j] * rr[j - 1];
+                rr[j] /= dd[j];
+            }
+        });
+}
+
+void planned_solve_pq_cpu(const Plan& P, const double* a, const double* b, double* d, double* rhs, bool transposed) {
+    const double* A = transposed ? b : a;
+    const double* U = transposed ? a : b;
+    walk_schedule(
+        P,
+        [&](int base, int gb) {
+            double* dd = d + base;
+            double* rr = rhs + base;
+            const double* AA = A + base;
+            const double* UU = U + base;
+            const int h = P.br_head[gb], e = P.br_end[gb];
+            double de = dd[e], re = rr[e];
+            for (int k = P.br_child_off[gb]; k < P.br_child_off[gb + 1]; k++) {
+                const int c = P.br_child[k];
+                de = std::fma(-(AA[c] * UU[c]), dd[c], de);
+                re = std::fma(-AA[c], rr[c], re);
+            }
+            double pp = de, qq = 1.0, yy = re;
+            for (int j = e; j > h; j--) {
+                const double pn = std::fma(dd[j - 1], pp, -((AA[j] * UU[j]) * qq));
+                const double yn = std::fma(rr[j - 1], pp, -(AA[j] * yy));
+                const double ip = 1.0 / pp;
+                dd[j] = qq * ip;
+                rr[j] = yy * ip;
+                qq = pp;
+                pp = pn;
+                yy = yn;
+                if (((e - j) & 3) == 3) {
+                    const double s = std::ldexp(1.0, -std::ilogb(pp));
+                    pp *= s;
+                    qq *= s;
+                    yy *= s;
+                }
+            }
+            const double ip = 1.0 / pp;
+            dd[h] = qq * ip;
+            rr[h] = yy * ip;
+        },
+        [&](int base, int gb) {
+            double* dd = d + base;
+            double* rr = rhs + base;
+            const double* UU = U + base;
+            const int h = P.br_head[gb], e = P.br_end[gb];
+            const int par = P.br_parent[gb];
+            double x = rr[h];
+            if (par >= 0) x = std::fma(-(UU[h] * dd[h]), rr[par], x);
+            rr[h] = x;
+            for (int j = h + 1; j <= e; j++) {
+                x = std::fma(-(UU[j] * dd[j]), x, rr[j]);
+                rr[j] = x;
+            }
+        });
 }
 
 }  // namespace hx

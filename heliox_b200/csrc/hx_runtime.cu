@@ -75,12 +75,14 @@ struct hx_ctx {
     hx::Plan P;
     double dt = 0.025, celsius = 6.3;
     // plan arrays
-    DevBuf<int> pack_node_off, pack_hh_off, pack_br_off, pack_lvl_off, pack_nlev, level_br_off;
+    DevBuf<int> pack_node_off, pack_slot_off, pack_br_off, pack_bch_off, pack_nch_off;
+    DevBuf<int> cs_node0, cs_nnode, cs_warp0, cs_nwarp, cs_bar, cs_lvl_off, cs_nlev, level_br_off;
     DevBuf<int> br_head, br_end, br_parent, br_child_off, br_child;
-    DevBuf<int> node_parent, node_child_off, node_child, node_hh, node_pas, node_ic_off, node_ic;
-    DevBuf<int> ref2gpu_node, ref2gpu_hh, ref2gpu_pas, ref2gpu_ic;
-    DevBuf<int> gpu2ref_node, gpu2ref_hh, gpu2ref_pas, gpu2ref_ic;
-    // parameters (GPU order); params[kind]
+    DevBuf<int> node_parent, node_child_off, node_child, node_flags, node_ic_off, node_ic;
+    // reference instance -> device index, per parameter kind (host + device copies)
+    std::vector<int> kmap_h[HX_P_COUNT];
+    DevBuf<int> kmap[HX_P_COUNT];
+    // parameters: node-indexed (density mechanisms, cm) or per IClamp instance
     DevBuf<double> a, b, area;
     DevBuf<double> prm[HX_P_COUNT];
     DevBuf<double> hh_ena, hh_ek, ic_del, ic_dur;
@@ -88,7 +90,7 @@ struct hx_ctx {
     // state, tape, checkpoints, adjoint, gradients
     DevBuf<double> sv, sm, sh, sn;
     DevBuf<double> tv, tm, th, tn;
-    DevBuf<double> ck;  // nseg x (nnode + 3 nhh)
+    DevBuf<double> ck;  // nseg x 4 nnode (v, m, h, n)
     DevBuf<double> lv, lm, lh, ln;
     DevBuf<double> grad;  // concatenated per kind
     size_t grad_off[HX_P_COUNT + 1] = {0};
@@ -138,18 +140,27 @@ static size_t kind_count(const hx::Plan& P, int kind) {
     return 0;
 }
 
-static const std::vector<int>& kind_gpu2ref(const hx::Plan& P, int kind) {
-    if (kind <= HX_P_HH_EL) return P.hh_gpu2ref;
-    if (kind <= HX_P_PAS_E) return P.pas_gpu2ref;
-    if (kind == HX_P_CM) return P.gpu2ref;
-    return P.ic_gpu2ref;
+// device storage length of a kind: node-indexed except IClamp amplitude
+static size_t kind_store(const hx::Plan& P, int kind) { return kind == HX_P_IC_AMP ? (size_t)P.nic : (size_t)P.nnode; }
+
+// dynamic shared memory per CTA of the two step kernels for a plan
+static void plan_smem(const hx::Plan& P, size_t& fwd, size_t& bwd) {
+    const size_t n = std::max(P.max_pack_nodes, 1);
+    const size_t lvl = (size_t)hx::kWarpsPerCta * (P.max_levels + 1);
+    const size_t ints = 3 * n + 1 + P.max_pack_nch + 4 * (size_t)P.max_pack_branches + 1 + P.max_pack_bch + lvl;
+    fwd = 8 * n * sizeof(double) + ints * sizeof(int);
+    bwd = 10 * n * sizeof(double) + ints * sizeof(int);
 }
 
-static int* kind_ref2gpu_dev(hx_ctx* c, int kind) {
-    if (kind <= HX_P_HH_EL) return c->ref2gpu_hh.p;
-    if (kind <= HX_P_PAS_E) return c->ref2gpu_pas.p;
-    if (kind == HX_P_CM) return c->ref2gpu_node.p;
-    return c->ref2gpu_ic.p;
+static void fill_stats(const hx::Plan& P, hx_plan_stats* out) {
+    out->npack = P.npack;
+    out->max_pack_nodes = P.max_pack_nodes;
+    out->max_pack_hh = P.max_pack_hh;
+    out->max_levels = P.max_levels;
+    out->max_crit_nodes = P.max_crit;
+    out->nbranch = (int)P.br_head.size();
+    out->imbalance = P.imbalance;
+    plan_smem(P, out->smem_fwd, out->smem_bwd);
 }
 
 static std::vector<int> invert(const std::vector<int>& g2r, size_t n) {
@@ -199,10 +210,10 @@ int hx_set_stream(hx_ctx* ctx, void* stream) {
     return 0;
 }
 
-int hx_set_pack_target(hx_ctx* ctx, int nodes_per_pack) {
+int hx_set_pack_target(hx_ctx* ctx, int nodes_per_warp) {
     if (!ctx) return -1;
-    if (nodes_per_pack < 0) return fail(ctx, "nodes_per_pack must be >= 0");
-    ctx->pack_target = nodes_per_pack;
+    if (nodes_per_warp < 0) return fail(ctx, "nodes_per_warp must be >= 0");
+    ctx->pack_target = nodes_per_warp;
     return 0;
 }
 
@@ -212,31 +223,22 @@ int hx_set_tape_budget(hx_ctx* ctx, size_t bytes) {
     return 0;
 }
 
-int hx_plan_check(const hx_group_desc* desc, int nodes_per_pack, hx_plan_stats* out, double* max_abs_diff) {
+int hx_plan_check(const hx_group_desc* desc, int nodes_per_warp, hx_plan_stats* out, double* max_abs_diff,
+                  double* pq_rel_diff) {
     if (!desc) return -1;
     hx::Plan P;
-    std::string e = hx::build_plan(*desc, nodes_per_pack, P);
+    std::string e = hx::build_plan(*desc, nodes_per_warp, 0, P);
     if (!e.empty()) {
         fprintf(stderr, "hx_plan_check: %s\n", e.c_str());
         return -2;
     }
-    if (out) {
-        out->npack = P.npack;
-        out->max_pack_nodes = P.max_pack_nodes;
-        out->max_pack_hh = P.max_pack_hh;
-        out->max_levels = P.max_levels;
-        out->max_crit_nodes = P.max_crit;
-        out->nbranch = (int)P.br_head.size();
-        out->imbalance = P.imbalance;
-        out->smem_fwd = sizeof(double) * (5 * (size_t)P.max_pack_nodes + 3 * (size_t)P.max_pack_hh);
-        out->smem_bwd = sizeof(double) * (7 * (size_t)P.max_pack_nodes + 3 * (size_t)P.max_pack_hh);
-    }
-    if (max_abs_diff) {
+    if (out) fill_stats(P, out);
+    if (max_abs_diff || pq_rel_diff) {
         // seeded diagonally dominant system; serial solve in reference order vs planned schedule
         const int n = desc->nnode;
         std::mt19937_64 rng(12345);
         std::uniform_real_distribution<double> U(0.5, 1.5);
-        double worst = 0.0;
+        double worst = 0.0, worst_pq = 0.0;
         for (int transposed = 0; transposed < 2; transposed++) {
             std::vector<double> d(n), r(n);
             for (int i = 0; i < n; i++) {
@@ -269,10 +271,18 @@ int hx_plan_check(const hx_group_desc* desc, int nodes_per_pack, hx_plan_stats* 
                 dg[gi] = d[ref];
                 rg[gi] = r[ref];
             }
+            std::vector<double> dq = dg, rq = rg;
             hx::planned_solve_cpu(P, ag.data(), bg.data(), dg.data(), rg.data(), transposed != 0);
-            for (int gi = 0; gi < n; gi++) worst = std::max(worst, std::fabs(rg[gi] - rs[P.gpu2ref[gi]]));
+            hx::planned_solve_pq_cpu(P, ag.data(), bg.data(), dq.data(), rq.data(), transposed != 0);
+            double scale = 0.0;
+            for (int gi = 0; gi < n; gi++) scale = std::max(scale, std::fabs(rs[gi]));
+            for (int gi = 0; gi < n; gi++) {
+                worst = std::max(worst, std::fabs(rg[gi] - rs[P.gpu2ref[gi]]));
+                worst_pq = std::max(worst_pq, std::fabs(rq[gi] - rs[P.gpu2ref[gi]]) / scale);
+            }
         }
-        *max_abs_diff = worst;
+        if (max_abs_diff) *max_abs_diff = worst;
+        if (pq_rel_diff) *pq_rel_diff = worst_pq;
     }
     return 0;
 }
@@ -282,17 +292,31 @@ int hx_load_group(hx_ctx* ctx, const hx_group_desc* desc) {
     HXC(cudaSetDevice(ctx->device));
     ctx->loaded = false;
     ctx->captured = false;
-    std::string e = hx::build_plan(*desc, ctx->pack_target, ctx->P);
+    ctx->probe_key.clear();
+    // per-CTA node capacity from the opt-in shared memory (backward kernel: 10
+    // doubles per node plus the topology tables, about 16 bytes per node)
+    int optin = 0;
+    HXC(cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, ctx->device));
+    const int cap_nodes = (int)((optin - 4096) / (10 * sizeof(double) + 20));
+    std::string e = hx::build_plan(*desc, ctx->pack_target, cap_nodes, ctx->P);
     if (!e.empty()) return fail(ctx, "invalid group: " + e);
     const hx::Plan& P = ctx->P;
     cudaStream_t st = ctx->st;
+    const size_t nn = P.nnode, nc = P.nic;
     ctx->dt = desc->dt;
     ctx->celsius = desc->celsius;
     HXC(ctx->pack_node_off.upload(P.pack_node_off, st));
-    HXC(ctx->pack_hh_off.upload(P.pack_hh_off, st));
+    HXC(ctx->pack_slot_off.upload(P.pack_slot_off, st));
     HXC(ctx->pack_br_off.upload(P.pack_br_off, st));
-    HXC(ctx->pack_lvl_off.upload(P.pack_lvl_off, st));
-    HXC(ctx->pack_nlev.upload(P.pack_nlev, st));
+    HXC(ctx->pack_bch_off.upload(P.pack_bch_off, st));
+    HXC(ctx->pack_nch_off.upload(P.pack_nch_off, st));
+    HXC(ctx->cs_node0.upload(P.cs_node0, st));
+    HXC(ctx->cs_nnode.upload(P.cs_nnode, st));
+    HXC(ctx->cs_warp0.upload(P.cs_warp0, st));
+    HXC(ctx->cs_nwarp.upload(P.cs_nwarp, st));
+    HXC(ctx->cs_bar.upload(P.cs_bar, st));
+    HXC(ctx->cs_lvl_off.upload(P.cs_lvl_off, st));
+    HXC(ctx->cs_nlev.upload(P.cs_nlev, st));
     HXC(ctx->level_br_off.upload(P.level_br_off, st));
     HXC(ctx->br_head.upload(P.br_head, st));
     HXC(ctx->br_end.upload(P.br_end, st));
@@ -302,67 +326,95 @@ int hx_load_group(hx_ctx* ctx, const hx_group_desc* desc) {
     HXC(ctx->node_parent.upload(P.node_parent, st));
     HXC(ctx->node_child_off.upload(P.node_child_off, st));
     HXC(ctx->node_child.upload(P.node_child, st));
-    HXC(ctx->node_hh.upload(P.node_hh, st));
-    HXC(ctx->node_pas.upload(P.node_pas, st));
     HXC(ctx->node_ic_off.upload(P.node_ic_off, st));
     HXC(ctx->node_ic.upload(P.node_ic, st));
-    HXC(ctx->gpu2ref_node.upload(P.gpu2ref, st));
-    HXC(ctx->ref2gpu_node.upload(P.ref2gpu, st));
-    HXC(ctx->gpu2ref_hh.upload(P.hh_gpu2ref.empty() ? std::vector<int>{0} : P.hh_gpu2ref, st));
-    HXC(ctx->gpu2ref_pas.upload(P.pas_gpu2ref.empty() ? std::vector<int>{0} : P.pas_gpu2ref, st));
-    HXC(ctx->gpu2ref_ic.upload(P.ic_gpu2ref.empty() ? std::vector<int>{0} : P.ic_gpu2ref, st));
-    HXC(ctx->ref2gpu_hh.upload(invert(P.hh_gpu2ref, P.nhh), st));
-    HXC(ctx->ref2gpu_pas.upload(invert(P.pas_gpu2ref, P.npas), st));
-    HXC(ctx->ref2gpu_ic.upload(invert(P.ic_gpu2ref, P.nic), st));
+    std::vector<int> flags(nn, 0);
+    for (size_t gi = 0; gi < nn; gi++)
+        flags[gi] = (P.node_pas[gi] >= 0 ? hx::kHasPas : 0) | (P.node_hh[gi] >= 0 ? hx::kHasHH : 0);
+    HXC(ctx->node_flags.upload(flags, st));
 
-    auto perm = [&](const double* src, const std::vector<int>& g2r, size_t n) {
-        std::vector<double> out(std::max<size_t>(n, 1), 0.0);
-        for (size_t i = 0; i < n; i++) out[i] = src[g2r[i]];
+    // reference instance -> device slot per kind
+    for (int k = 0; k < HX_P_COUNT; k++) {
+        std::vector<int>& m = ctx->kmap_h[k];
+        m.assign(std::max<size_t>(kind_count(P, k), 1), 0);
+        const size_t cnt = kind_count(P, k);
+        for (size_t r = 0; r < cnt; r++) {
+            if (k <= HX_P_HH_EL)
+                m[r] = P.ref2gpu[desc->hh_node[r]];
+            else if (k <= HX_P_PAS_E)
+                m[r] = P.ref2gpu[desc->pas_node[r]];
+            else if (k == HX_P_CM)
+                m[r] = P.ref2gpu[r];
+        }
+        if (k == HX_P_IC_AMP) {
+            std::vector<int> inv = invert(P.ic_gpu2ref, P.nic);
+            for (size_t r = 0; r < cnt; r++) m[r] = inv[r];
+        }
+        HXC(ctx->kmap[k].upload(m, st));
+    }
+    // node-indexed copies of reference-ordered arrays
+    auto node_arr = [&](const double* src) {
+        std::vector<double> out(std::max<size_t>(nn, 1), 0.0);
+        for (size_t gi = 0; gi < nn; gi++) out[gi] = src[P.gpu2ref[gi]];
         return out;
     };
-    const size_t nn = P.nnode, nh = P.nhh, np = P.npas, nc = P.nic;
-    HXC(ctx->a.upload(perm(desc->a, P.gpu2ref, nn), st));
-    HXC(ctx->b.upload(perm(desc->b, P.gpu2ref, nn), st));
-    HXC(ctx->area.upload(perm(desc->area, P.gpu2ref, nn), st));
-    HXC(ctx->prm[HX_P_CM].upload(perm(desc->cm, P.gpu2ref, nn), st));
-    HXC(ctx->prm[HX_P_HH_GNABAR].upload(perm(desc->hh_gnabar, P.hh_gpu2ref, nh), st));
-    HXC(ctx->prm[HX_P_HH_GKBAR].upload(perm(desc->hh_gkbar, P.hh_gpu2ref, nh), st));
-    HXC(ctx->prm[HX_P_HH_GL].upload(perm(desc->hh_gl, P.hh_gpu2ref, nh), st));
-    HXC(ctx->prm[HX_P_HH_EL].upload(perm(desc->hh_el, P.hh_gpu2ref, nh), st));
-    HXC(ctx->hh_ena.upload(perm(desc->hh_ena, P.hh_gpu2ref, nh), st));
-    HXC(ctx->hh_ek.upload(perm(desc->hh_ek, P.hh_gpu2ref, nh), st));
-    HXC(ctx->prm[HX_P_PAS_G].upload(perm(desc->pas_g, P.pas_gpu2ref, np), st));
-    HXC(ctx->prm[HX_P_PAS_E].upload(perm(desc->pas_e, P.pas_gpu2ref, np), st));
-    HXC(ctx->ic_del.upload(perm(desc->ic_del, P.ic_gpu2ref, nc), st));
-    HXC(ctx->ic_dur.upload(perm(desc->ic_dur, P.ic_gpu2ref, nc), st));
-    HXC(ctx->prm[HX_P_IC_AMP].upload(perm(desc->ic_amp, P.ic_gpu2ref, nc), st));
+    auto inst_arr = [&](int kind, const double* src) {  // density-mechanism instance values -> node slots
+        std::vector<double> out(std::max<size_t>(kind_store(P, kind), 1), 0.0);
+        const size_t cnt = kind_count(P, kind);
+        for (size_t r = 0; r < cnt; r++) out[ctx->kmap_h[kind][r]] = src[r];
+        return out;
+    };
+    HXC(ctx->a.upload(node_arr(desc->a), st));
+    HXC(ctx->b.upload(node_arr(desc->b), st));
+    HXC(ctx->area.upload(node_arr(desc->area), st));
+    HXC(ctx->prm[HX_P_CM].upload(node_arr(desc->cm), st));
+    HXC(ctx->prm[HX_P_HH_GNABAR].upload(inst_arr(HX_P_HH_GNABAR, desc->hh_gnabar), st));
+    HXC(ctx->prm[HX_P_HH_GKBAR].upload(inst_arr(HX_P_HH_GKBAR, desc->hh_gkbar), st));
+    HXC(ctx->prm[HX_P_HH_GL].upload(inst_arr(HX_P_HH_GL, desc->hh_gl), st));
+    HXC(ctx->prm[HX_P_HH_EL].upload(inst_arr(HX_P_HH_EL, desc->hh_el), st));
+    HXC(ctx->hh_ena.upload(inst_arr(HX_P_HH_GNABAR, desc->hh_ena), st));
+    HXC(ctx->hh_ek.upload(inst_arr(HX_P_HH_GNABAR, desc->hh_ek), st));
+    HXC(ctx->prm[HX_P_PAS_G].upload(inst_arr(HX_P_PAS_G, desc->pas_g), st));
+    HXC(ctx->prm[HX_P_PAS_E].upload(inst_arr(HX_P_PAS_E, desc->pas_e), st));
+    HXC(ctx->ic_del.upload(inst_arr(HX_P_IC_AMP, desc->ic_del), st));
+    HXC(ctx->ic_dur.upload(inst_arr(HX_P_IC_AMP, desc->ic_dur), st));
+    HXC(ctx->prm[HX_P_IC_AMP].upload(inst_arr(HX_P_IC_AMP, desc->ic_amp), st));
 
     HXC(ctx->sv.ensure(nn));
-    HXC(ctx->sm.ensure(nh));
-    HXC(ctx->sh.ensure(nh));
-    HXC(ctx->sn.ensure(nh));
+    HXC(ctx->sm.ensure(nn));
+    HXC(ctx->sh.ensure(nn));
+    HXC(ctx->sn.ensure(nn));
     HXC(ctx->lv.ensure(nn));
-    HXC(ctx->lm.ensure(nh));
-    HXC(ctx->lh.ensure(nh));
-    HXC(ctx->ln.ensure(nh));
+    HXC(ctx->lm.ensure(nn));
+    HXC(ctx->lh.ensure(nn));
+    HXC(ctx->ln.ensure(nn));
     ctx->grad_off[0] = 0;
-    for (int k = 0; k < HX_P_COUNT; k++) ctx->grad_off[k + 1] = ctx->grad_off[k] + kind_count(P, k);
+    for (int k = 0; k < HX_P_COUNT; k++) ctx->grad_off[k + 1] = ctx->grad_off[k] + kind_store(P, k);
     HXC(ctx->grad.ensure(ctx->grad_off[HX_P_COUNT]));
+    HXC(ctx->stage_dev.ensure(ctx->grad_off[HX_P_COUNT] + nn));
 
     hx::DevGroup& G = ctx->G;
     G = hx::DevGroup{};
     G.npack = P.npack;
     G.nnode = P.nnode;
-    G.nhh = P.nhh;
-    G.npas = P.npas;
     G.nic = P.nic;
     G.smem_n = std::max(P.max_pack_nodes, 1);
-    G.smem_nh = std::max(P.max_pack_hh, 1);
+    G.smem_br = P.max_pack_branches;
+    G.smem_bch = P.max_pack_bch;
+    G.smem_nch = P.max_pack_nch;
+    G.smem_lvl = hx::kWarpsPerCta * (P.max_levels + 1);
     G.pack_node_off = ctx->pack_node_off.p;
-    G.pack_hh_off = ctx->pack_hh_off.p;
+    G.pack_slot_off = ctx->pack_slot_off.p;
     G.pack_br_off = ctx->pack_br_off.p;
-    G.pack_lvl_off = ctx->pack_lvl_off.p;
-    G.pack_nlev = ctx->pack_nlev.p;
+    G.pack_bch_off = ctx->pack_bch_off.p;
+    G.pack_nch_off = ctx->pack_nch_off.p;
+    G.cs_node0 = ctx->cs_node0.p;
+    G.cs_nnode = ctx->cs_nnode.p;
+    G.cs_warp0 = ctx->cs_warp0.p;
+    G.cs_nwarp = ctx->cs_nwarp.p;
+    G.cs_bar = ctx->cs_bar.p;
+    G.cs_lvl_off = ctx->cs_lvl_off.p;
+    G.cs_nlev = ctx->cs_nlev.p;
     G.level_br_off = ctx->level_br_off.p;
     G.br_head = ctx->br_head.p;
     G.br_end = ctx->br_end.p;
@@ -372,8 +424,7 @@ int hx_load_group(hx_ctx* ctx, const hx_group_desc* desc) {
     G.node_parent = ctx->node_parent.p;
     G.node_child_off = ctx->node_child_off.p;
     G.node_child = ctx->node_child.p;
-    G.node_hh = ctx->node_hh.p;
-    G.node_pas = ctx->node_pas.p;
+    G.node_flags = ctx->node_flags.p;
     G.node_ic_off = ctx->node_ic_off.p;
     G.node_ic = ctx->node_ic.p;
     G.a = ctx->a.p;
@@ -392,8 +443,8 @@ int hx_load_group(hx_ctx* ctx, const hx_group_desc* desc) {
     G.ic_dur = ctx->ic_dur.p;
     G.ic_amp = ctx->prm[HX_P_IC_AMP].p;
     G.dt = desc->dt;
-    G.cfac = 0.001 * (1.0 / desc->dt);                   // capac.cpp:56,70 with cj = 1/dt
-    G.q10 = std::pow(3.0, (desc->celsius - 6.3) / 10);   // hh_templated.cu:90
+    G.cfac = 0.001 * (1.0 / desc->dt);                  // capac.cpp:56,70 with cj = 1/dt
+    G.q10 = std::pow(3.0, (desc->celsius - 6.3) / 10);  // hh_templated.cu:90
     size_t sf = hx::fwd_smem_bytes(G), sb = hx::bwd_smem_bytes(G);
     int maxsmem = 0;
     HXC(cudaDeviceGetAttribute(&maxsmem, cudaDevAttrMaxSharedMemoryPerBlockOptin, ctx->device));
@@ -409,16 +460,7 @@ int hx_load_group(hx_ctx* ctx, const hx_group_desc* desc) {
 int hx_get_plan_stats(hx_ctx* ctx, hx_plan_stats* out) {
     if (!ctx || !out) return -1;
     if (!ctx->loaded) return fail(ctx, "no group loaded");
-    const hx::Plan& P = ctx->P;
-    out->npack = P.npack;
-    out->max_pack_nodes = P.max_pack_nodes;
-    out->max_pack_hh = P.max_pack_hh;
-    out->max_levels = P.max_levels;
-    out->max_crit_nodes = P.max_crit;
-    out->nbranch = (int)P.br_head.size();
-    out->imbalance = P.imbalance;
-    out->smem_fwd = hx::fwd_smem_bytes(ctx->G);
-    out->smem_bwd = hx::bwd_smem_bytes(ctx->G);
+    fill_stats(ctx->P, out);
     return 0;
 }
 
@@ -426,16 +468,16 @@ int hx_set_param(hx_ctx* ctx, int kind, const double* values, int n) {
     if (!ctx || !values) return fail(ctx, "null argument");
     if (!ctx->loaded) return fail(ctx, "no group loaded");
     if (kind < 0 || kind >= HX_P_COUNT) return fail(ctx, "bad parameter kind");
-    size_t cnt = kind_count(ctx->P, kind);
+    const size_t cnt = kind_count(ctx->P, kind);
     if ((size_t)n != cnt) return fail(ctx, "parameter count mismatch");
     if (!cnt) return 0;
     HXC(cudaSetDevice(ctx->device));
     HXC(ctx->pin.ensure(cnt * sizeof(double)));
-    double* h = (double*)ctx->pin.p;
-    const std::vector<int>& g2r = kind_gpu2ref(ctx->P, kind);
-    HXC(cudaStreamSynchronize(ctx->st));  // pinned staging buffer may still be in use
-    for (size_t i = 0; i < cnt; i++) h[i] = values[g2r[i]];
-    HXC(cudaMemcpyAsync(ctx->prm[kind].p, h, cnt * sizeof(double), cudaMemcpyHostToDevice, ctx->st));
+    HXC(cudaStreamSynchronize(ctx->st));  // the pinned staging buffer may still be in flight
+    memcpy(ctx->pin.p, values, cnt * sizeof(double));
+    double* stage = ctx->stage_dev.p;
+    HXC(cudaMemcpyAsync(stage, ctx->pin.p, cnt * sizeof(double), cudaMemcpyHostToDevice, ctx->st));
+    HXC(hx::launch_scatter(stage, ctx->kmap[kind].p, ctx->prm[kind].p, (int)cnt, ctx->st));
     HXC(cudaStreamSynchronize(ctx->st));
     return 0;
 }
@@ -444,12 +486,11 @@ int hx_get_param(hx_ctx* ctx, int kind, double* values, int n) {
     if (!ctx || !values) return fail(ctx, "null argument");
     if (!ctx->loaded) return fail(ctx, "no group loaded");
     if (kind < 0 || kind >= HX_P_COUNT) return fail(ctx, "bad parameter kind");
-    size_t cnt = kind_count(ctx->P, kind);
+    const size_t cnt = kind_count(ctx->P, kind);
     if ((size_t)n != cnt) return fail(ctx, "parameter count mismatch");
     if (!cnt) return 0;
     HXC(cudaSetDevice(ctx->device));
-    HXC(ctx->stage_dev.ensure(cnt));
-    HXC(hx::launch_gather(ctx->prm[kind].p, kind_ref2gpu_dev(ctx, kind), ctx->stage_dev.p, (int)cnt, ctx->st));
+    HXC(hx::launch_gather(ctx->prm[kind].p, ctx->kmap[kind].p, ctx->stage_dev.p, (int)cnt, ctx->st));
     HXC(cudaMemcpyAsync(values, ctx->stage_dev.p, cnt * sizeof(double), cudaMemcpyDeviceToHost, ctx->st));
     HXC(cudaStreamSynchronize(ctx->st));
     return 0;
@@ -515,13 +556,13 @@ static int setup_time(hx_ctx* ctx, int nstep) {
 }
 
 static int plan_tape(hx_ctx* ctx, int nstep) {
-    const size_t nn = ctx->P.nnode, nh = ctx->P.nhh;
-    const size_t per_step = (nn + 3 * nh) * sizeof(double);
+    const size_t nn = ctx->P.nnode;
+    const size_t per_step = 4 * nn * sizeof(double);  // v, m, h, n
     size_t budget = ctx->tape_budget;
     if (!budget) {
         size_t fr = 0, tot = 0;
         HXC(cudaMemGetInfo(&fr, &tot));
-        budget = (size_t)(0.6 * (double)(fr + ctx->tv.n * sizeof(double) + 3 * ctx->tm.n * sizeof(double)));
+        budget = (size_t)(0.6 * (double)(fr + 4 * ctx->tv.n * sizeof(double)));
     }
     const size_t full = per_step * (size_t)(nstep + 1);
     if (full <= budget) {
@@ -529,12 +570,12 @@ static int plan_tape(hx_ctx* ctx, int nstep) {
         ctx->seg = nstep;
         ctx->nseg = 1;
         HXC(ctx->tv.ensure(nn * (size_t)(nstep + 1)));
-        HXC(ctx->tm.ensure(nh * (size_t)nstep + 1));
-        HXC(ctx->th.ensure(nh * (size_t)nstep + 1));
-        HXC(ctx->tn.ensure(nh * (size_t)nstep + 1));
+        HXC(ctx->tm.ensure(nn * (size_t)(nstep + 1)));
+        HXC(ctx->th.ensure(nn * (size_t)(nstep + 1)));
+        HXC(ctx->tn.ensure(nn * (size_t)(nstep + 1)));
         return 0;
     }
-    // checkpointed: segments of K steps; K*per_step (segment tape) + nseg*per_step (checkpoints) <= budget
+    // checkpointed: segments of K steps; (K+1) tape rows + one checkpoint per segment within budget
     size_t K = (size_t)std::sqrt((double)nstep);
     if (K < 1) K = 1;
     while (K > 1 && (K + 1 + ((size_t)nstep + K - 1) / K) * per_step > budget) K /= 2;
@@ -544,35 +585,24 @@ static int plan_tape(hx_ctx* ctx, int nstep) {
     ctx->seg = (int)K;
     ctx->nseg = (int)(((size_t)nstep + K - 1) / K);
     HXC(ctx->tv.ensure(nn * (K + 1)));
-    HXC(ctx->tm.ensure(nh * K + 1));
-    HXC(ctx->th.ensure(nh * K + 1));
-    HXC(ctx->tn.ensure(nh * K + 1));
-    HXC(ctx->ck.ensure((nn + 3 * nh) * (size_t)ctx->nseg));
+    HXC(ctx->tm.ensure(nn * (K + 1)));
+    HXC(ctx->th.ensure(nn * (K + 1)));
+    HXC(ctx->tn.ensure(nn * (K + 1)));
+    HXC(ctx->ck.ensure(4 * nn * (size_t)ctx->nseg));
     return 0;
 }
 
 static hx::DevState state_view(hx_ctx* c) { return hx::DevState{c->sv.p, c->sm.p, c->sh.p, c->sn.p}; }
 
-static int save_ck(hx_ctx* ctx, int s) {
-    const size_t nn = ctx->P.nnode, nh = ctx->P.nhh;
-    double* base = ctx->ck.p + (nn + 3 * nh) * (size_t)s;
-    HXC(cudaMemcpyAsync(base, ctx->sv.p, nn * 8, cudaMemcpyDeviceToDevice, ctx->st));
-    if (nh) {
-        HXC(cudaMemcpyAsync(base + nn, ctx->sm.p, nh * 8, cudaMemcpyDeviceToDevice, ctx->st));
-        HXC(cudaMemcpyAsync(base + nn + nh, ctx->sh.p, nh * 8, cudaMemcpyDeviceToDevice, ctx->st));
-        HXC(cudaMemcpyAsync(base + nn + 2 * nh, ctx->sn.p, nh * 8, cudaMemcpyDeviceToDevice, ctx->st));
-    }
-    return 0;
-}
-
-static int load_ck(hx_ctx* ctx, int s) {
-    const size_t nn = ctx->P.nnode, nh = ctx->P.nhh;
-    const double* base = ctx->ck.p + (nn + 3 * nh) * (size_t)s;
-    HXC(cudaMemcpyAsync(ctx->sv.p, base, nn * 8, cudaMemcpyDeviceToDevice, ctx->st));
-    if (nh) {
-        HXC(cudaMemcpyAsync(ctx->sm.p, base + nn, nh * 8, cudaMemcpyDeviceToDevice, ctx->st));
-        HXC(cudaMemcpyAsync(ctx->sh.p, base + nn + nh, nh * 8, cudaMemcpyDeviceToDevice, ctx->st));
-        HXC(cudaMemcpyAsync(ctx->sn.p, base + nn + 2 * nh, nh * 8, cudaMemcpyDeviceToDevice, ctx->st));
+static int copy_ck(hx_ctx* ctx, int s, bool save) {
+    const size_t nn = ctx->P.nnode;
+    double* base = ctx->ck.p + 4 * nn * (size_t)s;
+    double* st[4] = {ctx->sv.p, ctx->sm.p, ctx->sh.p, ctx->sn.p};
+    for (int k = 0; k < 4; k++) {
+        if (save)
+            HXC(cudaMemcpyAsync(base + k * nn, st[k], nn * 8, cudaMemcpyDeviceToDevice, ctx->st));
+        else
+            HXC(cudaMemcpyAsync(st[k], base + k * nn, nn * 8, cudaMemcpyDeviceToDevice, ctx->st));
     }
     return 0;
 }
@@ -599,7 +629,7 @@ static int run_forward(hx_ctx* ctx, int nstep, double v_init, int nprobe, const 
         launches = 1;
     } else {
         for (int s = 0; s < ctx->nseg; s++) {
-            if (save_ck(ctx, s)) return -1;
+            if (copy_ck(ctx, s, true)) return -1;
             int k0 = s * ctx->seg, k1 = std::min(nstep, k0 + ctx->seg);
             HXC(hx::launch_fwd(ctx->G, S, T, 0, PV, trace_dev, ctx->tmid.p, k0, k1, ctx->st));
             launches++;
@@ -616,13 +646,11 @@ static int run_backward(hx_ctx* ctx, const double* dLdv_dev) {
     if (!ctx->loaded) return fail(ctx, "no group loaded");
     if (!ctx->captured) return fail(ctx, "hx_backward needs a preceding hx_forward_capture");
     HXC(cudaSetDevice(ctx->device));
-    const size_t nn = ctx->P.nnode, nh = ctx->P.nhh;
+    const size_t nn = ctx->P.nnode;
     HXC(cudaMemsetAsync(ctx->lv.p, 0, nn * 8, ctx->st));
-    if (nh) {
-        HXC(cudaMemsetAsync(ctx->lm.p, 0, nh * 8, ctx->st));
-        HXC(cudaMemsetAsync(ctx->lh.p, 0, nh * 8, ctx->st));
-        HXC(cudaMemsetAsync(ctx->ln.p, 0, nh * 8, ctx->st));
-    }
+    HXC(cudaMemsetAsync(ctx->lm.p, 0, nn * 8, ctx->st));
+    HXC(cudaMemsetAsync(ctx->lh.p, 0, nn * 8, ctx->st));
+    HXC(cudaMemsetAsync(ctx->ln.p, 0, nn * 8, ctx->st));
     HXC(cudaMemsetAsync(ctx->grad.p, 0, ctx->grad_off[HX_P_COUNT] * 8, ctx->st));
     hx::DevAdj A{ctx->lv.p, ctx->lm.p, ctx->lh.p, ctx->ln.p};
     double* g = ctx->grad.p;
@@ -640,7 +668,7 @@ static int run_backward(hx_ctx* ctx, const double* dLdv_dev) {
     } else {
         for (int s = ctx->nseg - 1; s >= 0; s--) {
             int k0 = s * ctx->seg, k1 = std::min(ctx->nstep, k0 + ctx->seg);
-            if (load_ck(ctx, s)) return -1;
+            if (copy_ck(ctx, s, false)) return -1;
             hx::DevTape T{ctx->tv.p, ctx->tm.p, ctx->th.p, ctx->tn.p, k0};
             HXC(hx::launch_fwd(ctx->G, S, T, 1, PV, nullptr, ctx->tmid.p, k0, k1, ctx->st));
             HXC(hx::launch_bwd(ctx->G, T, A, GR, PV, dLdv_dev, ctx->tmid.p, k1, k0, ctx->st));
@@ -652,12 +680,13 @@ static int run_backward(hx_ctx* ctx, const double* dLdv_dev) {
     return 0;
 }
 
+// per-kind gradients in reference instance order into device buffers
 static int gather_grads_dev(hx_ctx* ctx, double* const* grads_dev) {
     if (!grads_dev) return 0;
     for (int k = 0; k < HX_P_COUNT; k++) {
         if (!grads_dev[k]) continue;
-        size_t cnt = kind_count(ctx->P, k);
-        HXC(hx::launch_gather(ctx->grad.p + ctx->grad_off[k], kind_ref2gpu_dev(ctx, k), grads_dev[k], (int)cnt, ctx->st));
+        const size_t cnt = kind_count(ctx->P, k);
+        HXC(hx::launch_gather(ctx->grad.p + ctx->grad_off[k], ctx->kmap[k].p, grads_dev[k], (int)cnt, ctx->st));
     }
     return 0;
 }
@@ -666,7 +695,7 @@ extern "C" {
 
 int hx_simulate(hx_ctx* ctx, int nstep, double v_init, int nprobe, const int* probe_nodes, double* trace) {
     if (!ctx) return -1;
-    size_t tn = (size_t)(nstep + 1) * (size_t)nprobe;
+    const size_t tn = (size_t)(nstep + 1) * (size_t)nprobe;
     HXC(ctx->trace_dev.ensure(tn));
     if (run_forward(ctx, nstep, v_init, nprobe, probe_nodes, ctx->trace_dev.p, false)) return -1;
     if (trace && tn) HXC(cudaMemcpyAsync(trace, ctx->trace_dev.p, tn * 8, cudaMemcpyDeviceToHost, ctx->st));
@@ -676,7 +705,7 @@ int hx_simulate(hx_ctx* ctx, int nstep, double v_init, int nprobe, const int* pr
 
 int hx_forward_capture(hx_ctx* ctx, int nstep, double v_init, int nprobe, const int* probe_nodes, double* trace) {
     if (!ctx) return -1;
-    size_t tn = (size_t)(nstep + 1) * (size_t)nprobe;
+    const size_t tn = (size_t)(nstep + 1) * (size_t)nprobe;
     HXC(ctx->trace_dev.ensure(tn));
     if (run_forward(ctx, nstep, v_init, nprobe, probe_nodes, ctx->trace_dev.p, true)) return -1;
     if (trace && tn) HXC(cudaMemcpyAsync(trace, ctx->trace_dev.p, tn * 8, cudaMemcpyDeviceToHost, ctx->st));
@@ -693,18 +722,17 @@ int hx_forward_capture_dev(hx_ctx* ctx, int nstep, double v_init, int nprobe, co
 int hx_backward(hx_ctx* ctx, const double* dLdv, double* const* grads) {
     if (!ctx || !dLdv) return fail(ctx, "null argument");
     if (!ctx->captured) return fail(ctx, "hx_backward needs a preceding hx_forward_capture");
-    size_t tn = (size_t)(ctx->nstep + 1) * (size_t)ctx->nprobe;
+    const size_t tn = (size_t)(ctx->nstep + 1) * (size_t)ctx->nprobe;
     HXC(ctx->dLdv_dev.ensure(tn));
     if (tn) HXC(cudaMemcpyAsync(ctx->dLdv_dev.p, dLdv, tn * 8, cudaMemcpyHostToDevice, ctx->st));
     if (run_backward(ctx, ctx->dLdv_dev.p)) return -1;
     if (grads) {
-        HXC(ctx->stage_dev.ensure(ctx->grad_off[HX_P_COUNT]));
         for (int k = 0; k < HX_P_COUNT; k++) {
             if (!grads[k]) continue;
-            size_t cnt = kind_count(ctx->P, k);
+            const size_t cnt = kind_count(ctx->P, k);
             if (!cnt) continue;
             double* sd = ctx->stage_dev.p + ctx->grad_off[k];
-            HXC(hx::launch_gather(ctx->grad.p + ctx->grad_off[k], kind_ref2gpu_dev(ctx, k), sd, (int)cnt, ctx->st));
+            HXC(hx::launch_gather(ctx->grad.p + ctx->grad_off[k], ctx->kmap[k].p, sd, (int)cnt, ctx->st));
             HXC(cudaMemcpyAsync(grads[k], sd, cnt * 8, cudaMemcpyDeviceToHost, ctx->st));
         }
     }
@@ -733,25 +761,12 @@ int hx_reduce_grads_f32(hx_ctx* ctx, int n, const int* kind, const int* index, c
     }
     for (int c = 0; c < n_out; c++) cnt[c + 1] += cnt[c];
     // entries grouped by destination column, stable in input order; each entry
-    // points at (offset of its kind) + (GPU index of its reference instance)
+    // points at (offset of its kind) + (device slot of its reference instance)
     std::vector<int> flat(std::max(n, 1)), fill(cnt.begin(), cnt.end() - 1);
     std::vector<float> sc(std::max(n, 1));
-    const std::vector<int> inv_hh = invert(ctx->P.hh_gpu2ref, ctx->P.nhh);
-    const std::vector<int> inv_pas = invert(ctx->P.pas_gpu2ref, ctx->P.npas);
-    const std::vector<int> inv_ic = invert(ctx->P.ic_gpu2ref, ctx->P.nic);
     for (int e = 0; e < n; e++) {
         const int pos = fill[dest[e]]++;
-        const int k = kind[e], r = index[e];
-        int gi;
-        if (k <= HX_P_HH_EL)
-            gi = inv_hh[r];
-        else if (k <= HX_P_PAS_E)
-            gi = inv_pas[r];
-        else if (k == HX_P_CM)
-            gi = ctx->P.ref2gpu[r];
-        else
-            gi = inv_ic[r];
-        flat[pos] = (int)ctx->grad_off[k] + gi;
+        flat[pos] = (int)ctx->grad_off[kind[e]] + ctx->kmap_h[kind[e]][index[e]];
         sc[pos] = scale[e];
     }
     HXC(ctx->red_off.upload(cnt, ctx->st));

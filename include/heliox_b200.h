@@ -63,7 +63,7 @@ enum hx_param_kind {
 
 /* Statistics of the execution plan built at load time. */
 typedef struct hx_plan_stats {
-    int npack;            /* CTAs (cell packs) */
+    int npack;            /* CTAs (cell packs of 8 warps) */
     int max_pack_nodes;   /* largest pack */
     int max_pack_hh;
     int max_levels;       /* branch levels of the deepest pack */
@@ -82,8 +82,10 @@ const char* hx_last_error(hx_ctx* ctx);
 int hx_abi_version(void);
 /* Launch on this CUDA stream (cudaStream_t passed as void*); NULL = the context's own stream. */
 int hx_set_stream(hx_ctx* ctx, void* stream);
-/* Target nodes per cell pack (CTA); 0 = default.  Must be called before hx_load_group. */
-int hx_set_pack_target(hx_ctx* ctx, int nodes_per_pack);
+/* Target cell nodes per warp (0 = default 144): a cell of n nodes is advanced
+ * by ceil(n/target) warps (at most 8); cells are packed first-fit into 8-warp
+ * CTAs.  Must be called before hx_load_group. */
+int hx_set_pack_target(hx_ctx* ctx, int nodes_per_warp);
 /* Upper bound on device bytes the forward tape may use; when the full tape
  * does not fit, the backward recomputes checkpointed segments.  0 = default
  * (60% of free device memory at load time). */
@@ -95,11 +97,14 @@ int hx_set_tape_budget(hx_ctx* ctx, size_t bytes);
 int hx_load_group(hx_ctx* ctx, const hx_group_desc* desc);
 int hx_get_plan_stats(hx_ctx* ctx, hx_plan_stats* out);
 /* Build the execution plan on the host only (no device needed): validates the
- * group, reports statistics and checks, on the CPU, that the planned branch
- * schedule reproduces solve_serial (src/simulate.cpp:558-581) bit for bit on
- * seeded diagonally dominant systems.  *max_abs_diff receives the largest
- * difference (0 when bit-exact). */
-int hx_plan_check(const hx_group_desc* desc, int nodes_per_pack, hx_plan_stats* out, double* max_abs_diff);
+ * group, reports statistics and checks, on the CPU, the planned branch
+ * schedule against solve_serial (src/simulate.cpp:558-581) on seeded
+ * diagonally dominant systems, forward and transposed.  *max_abs_diff: largest
+ * difference of the schedule replayed in the reference's division form (0 when
+ * bit-exact).  *pq_rel_diff: largest difference, relative to max |x|, of the
+ * division-free form the kernels use. */
+int hx_plan_check(const hx_group_desc* desc, int nodes_per_warp, hx_plan_stats* out, double* max_abs_diff,
+                  double* pq_rel_diff);
 
 /* Parameter access in reference instance order (replaces the handle-based
  * Sim.set/get_variable path, src/python_api/PyBindings.cpp:80-81). */

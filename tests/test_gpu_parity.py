@@ -62,7 +62,7 @@ def test_forward_ball_and_stick(Sim):
 
 def test_forward_random_trees(Sim):
     g = synth.random_tree_batch(12, seed0=101)
-    s = Sim(0, pack_target=1500)
+    s = Sim(0, pack_target=200)
     s.load_group(g)
     rng = np.random.default_rng(0)
     probes = np.concatenate([g.soma_nodes(), rng.integers(g.ncell, g.nnode, 8)]).astype(np.int32)

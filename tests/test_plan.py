@@ -70,16 +70,19 @@ def test_planned_solve_bit_exact(maker, target):
     g = maker()
     stats, diff = _lib.plan_check(g, target)
     assert diff == 0.0
+    assert stats["pq_rel_diff"] <= 1e-13
     assert stats["npack"] >= 1
     assert stats["max_pack_nodes"] >= 1
 
 
 def test_packing_balance_and_coverage():
     g = synth.random_tree_batch(96, seed0=3)
-    stats, diff = _lib.plan_check(g, 1024)
+    stats, diff = _lib.plan_check(g, 0)
     assert diff == 0.0
-    assert stats["imbalance"] < 1.35
+    # packs hold whole cells in 8-warp CTAs; node counts stay within 1.6x of the mean
+    assert stats["imbalance"] < 1.6
     assert stats["nbranch"] >= g.ncell
+    assert stats["max_pack_nodes"] >= 1000 or stats["npack"] == 1
 
 
 def test_invalid_group_rejected():
