@@ -1,0 +1,409 @@
+#!/usr/bin/env python
+"""Benchmark of the hot path: forward + exact adjoint of a cell batch (config 2).
+
+One step = forward with tape (4000 fixed steps of dt 0.025 ms) over 1024
+seeded random-tree cells (hh + pas, somatic IClamp), the soma-voltage MSE
+against a teacher trace (conductances perturbed lognormally, sigma 0.2) and the
+reverse sweep producing every per-compartment conductance gradient.  The
+metric is forward+backward compartment-timesteps per second.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Multi-GPU runs are launched by torchrun, one process per GPU; every rank
+integrates its own 1024-cell batch (cells are independent: weak scaling, no
+data-path collective) and the time is the max over ranks.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "fwd+bwd compartment-timesteps/sec"
+UNIT = "comp-steps/s"
+T_STEPS = 4000
+NCELL = 1024
+SEED0 = 20240
+# DRAM bytes per compartment-step of the backward kernel from the committed ncu
+# capture (profiles/fwd_bwd_kernels_trees296.md: dram__bytes_read.sum +
+# dram__bytes_write.sum over the captured launch / its compartment-steps).
+BWD_DRAM_BYTES_PER_UNIT = 34.7
+
+
+def _alg_bytes(g):
+    """Algorithmic HBM bytes per timestep for the whole group, split forward/backward.
+
+    Per compartment B_c = 8*(3 p_c + 8 s_c) + 12 (p_c parameters, s_c states):
+    one forward, one checkpoint-recompute forward and one adjoint step.  The
+    forward kernel's share is 8*(p_c + 2 s_c) + 4, the backward's the rest.
+    """
+    import numpy as np
+
+    hh = np.zeros(g.nnode, bool)
+    hh[g.hh.nodes] = True
+    pas = np.zeros(g.nnode, bool)
+    pas[g.pas.nodes] = True
+    p = 3 + 4 * hh + 2 * pas
+    s = 1 + 3 * hh
+    fwd = 8 * (p + 2 * s) + 4
+    tot = 8 * (3 * p + 8 * s) + 12
+    return float(fwd.sum()), float((tot - fwd).sum()), float(tot.sum())
+
+
+def _peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle-reason sampling during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, phys_index: int):
+        self.idx = phys_index
+        self.proc = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "--query-gpu=" + self.FIELDS, "--format=csv,noheader,nounits", "-lms", "200",
+                 "-i", str(self.idx)], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            out, _ = self.proc.communicate(timeout=10)
+        except Exception:
+            self.proc.kill()
+            out, _ = self.proc.communicate()
+        sm, smax, reasons = [], None, set()
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        for line in out.strip().splitlines():
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                smax = float(parts[2])
+            except ValueError:
+                continue
+            for nm, v in zip(names, parts[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(nm)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": smax, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def _dist():
+    ws = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return ws, rank, local
+
+
+# ----------------------------------------------------------------------------- CPU baseline
+def _cpu_cell_job(args):
+    seed, nstep = args
+    sys.path.insert(0, ROOT)
+    import numpy as np
+
+    from heliox_b200 import synth
+    from oracle import oracle as O
+
+    g = synth.random_tree_cell(seed)
+    t0 = time.perf_counter()
+    tr, _ = O.forward(g, nstep)
+    dLdv = np.zeros_like(tr)
+    dLdv[1:] = 2.0 * tr[1:] / nstep
+    O.adjoint(g, nstep, dLdv)
+    return g.nnode * nstep, time.perf_counter() - t0
+
+
+def cpu_baseline(ncell_sample: int, nstep: int, procs: int):
+    """Oracle forward + adjoint on host cores; spawn pool (no CUDA in the workers)."""
+    import multiprocessing as mp
+
+    ctx = mp.get_context("spawn")
+    jobs = [(SEED0 + c, nstep) for c in range(ncell_sample)]
+    t0 = time.perf_counter()
+    with ctx.Pool(procs) as pool:
+        res = pool.map(_cpu_cell_job, jobs)
+    wall = time.perf_counter() - t0
+    units = sum(r[0] for r in res)
+    return units / wall, units, wall
+
+
+def _ref_kind():
+    from oracle import oracle as O
+
+    return "reference" if O.ref_available() else "port"
+
+
+# ----------------------------------------------------------------------------- reference arm
+def run_reference(args):
+    ws, rank, local = _dist()
+    if rank != 0:
+        return 0
+    procs = os.cpu_count() or 1
+    kind = _ref_kind()
+    vals = []
+    sample = 2 * max(procs, 8)
+    for it in range(args.warmup + args.steps):
+        v, units, wall = cpu_baseline(sample, T_STEPS, procs)
+        if it >= args.warmup:
+            vals.append(v)
+    value = statistics.median(vals)
+    line = {
+        "impl": "reference",
+        "metric": METRIC,
+        "value": value,
+        "unit": UNIT,
+        "n_gpus": args.gpus,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "f64",
+        "data": "synthetic",
+        "config": {"workload": f"config2: {NCELL} random-tree cells x {T_STEPS} steps, fwd+bwd",
+                   "sample": f"{sample} cells x {T_STEPS} steps per step"},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": procs, "kind": kind,
+                         "sample": f"{sample} cells of the config-2 batch, {T_STEPS} steps, forward + adjoint"},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# ----------------------------------------------------------------------------- our arm
+def run_ours(args):
+    import numpy as np
+    import torch
+
+    from heliox_b200 import synth
+    from heliox_b200.runtime import Sim
+
+    ws, rank, local = _dist()
+    dist = None
+    if ws > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    # an explicit stream: the legacy default stream (handle 0) would not order
+    # the library's launches against the timing events
+    stream = torch.cuda.Stream(dev)
+    torch.cuda.set_stream(stream)
+
+    # ---- synthetic workload (per rank: its own cells)
+    seed0 = SEED0 + 100000 * rank
+    g = synth.random_tree_batch(args.ncell, seed0=seed0)
+    teacher = synth.perturb_conductances(g, 0.2, seed=seed0 + 7)
+    T = args.nstep
+    ncomp = g.nnode
+    keys = ("hh.gnabar", "hh.gkbar", "hh.gl", "pas.g")
+
+    tsim = Sim(local)
+    tsim.load_group(teacher)
+    target_h = tsim.simulate(T)
+    tsim.close()
+    del tsim
+
+    s = Sim(local)
+    s.set_stream(stream.cuda_stream)
+    s.load_group(g)
+    target = torch.from_numpy(target_h).to(dev)
+    trace = torch.empty_like(target)
+    dLdv = torch.empty_like(target)
+    loss = torch.zeros(1, dtype=torch.float64, device=dev)
+    counts = {"hh.gnabar": g.hh.n, "hh.gkbar": g.hh.n, "hh.gl": g.hh.n, "pas.g": g.pas.n}
+    grads = {k: torch.empty(n, dtype=torch.float64, device=dev) for k, n in counts.items()}
+    flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=dev)  # > L2 (126 MB)
+
+    def step(ev=None):
+        if ev is not None:
+            ev[0].record(stream)
+        s.forward_capture_dev(T, trace.data_ptr())
+        if ev is not None:
+            ev[1].record(stream)
+        s.mse_loss_grad_dev(trace.data_ptr(), target.data_ptr(), T + 1, g.ncell, dLdv.data_ptr(), loss.data_ptr())
+        if ev is not None:
+            ev[2].record(stream)
+        s.backward_dev(dLdv.data_ptr(), {k: v.data_ptr() for k, v in grads.items()})
+        if ev is not None:
+            ev[3].record(stream)
+
+    for _ in range(args.warmup):
+        step()
+        flush.fill_(1.0)
+    torch.cuda.synchronize()
+
+    phys = local
+    cvd = os.environ.get("CUDA_VISIBLE_DEVICES")
+    if cvd:
+        try:
+            phys = int(cvd.split(",")[local])
+        except ValueError:
+            phys = local
+    sampler = ClockSampler(phys)
+    sampler.start()
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(args.steps)]
+    t_start = torch.cuda.Event(enable_timing=True)
+    t_end = torch.cuda.Event(enable_timing=True)
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    t_start.record(stream)
+    for k in range(args.steps):
+        step(evs[k])
+        flush.fill_(1.0)  # L2 flush between timed steps
+    t_end.record(stream)
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    clocks = sampler.stop()
+    ms = t_start.elapsed_time(t_end)
+    fwd_ms = statistics.mean(e[0].elapsed_time(e[1]) for e in evs)
+    bwd_ms = statistics.mean(e[2].elapsed_time(e[3]) for e in evs)
+    loss_val = float(loss.item())
+    # launches of our kernels per step: init, forward, MSE (2), backward, 4 gradient gathers
+    gpu_launches = args.steps * (1 + 1 + 2 + 1 + len(keys))
+
+    # ---- end to end through the public host-buffer API (params in, loss/grads out)
+    host_params = {k: np.ascontiguousarray(s.get_param_array(k)) for k in keys}
+    s.set_stream(0)
+    torch.cuda.synchronize()
+    h2d = sum(v.nbytes for v in host_params.values()) + (T + 1) * g.ncell * 8
+    d2h = (T + 1) * g.ncell * 8 + sum(8 * counts[k] for k in keys)
+    if dist:
+        dist.barrier()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        for k in keys:
+            s.set_param_array(k, host_params[k])
+        tr = s.forward_capture(T)
+        err = tr - target_h
+        dl = (2.0 / (T * g.ncell)) * err
+        dl[0] = 0.0
+        gg = s.backward(dl, keys=keys)
+    e2e_s = time.perf_counter() - t0
+    if dist:
+        dist.barrier()
+
+    # ---- max over ranks
+    vals = torch.tensor([ms, e2e_s, fwd_ms, bwd_ms, float(ncomp)], dtype=torch.float64, device=dev)
+    if dist:
+        mx = vals.clone()
+        dist.all_reduce(mx, op=dist.ReduceOp.MAX)
+        tot = vals.clone()
+        dist.all_reduce(tot, op=dist.ReduceOp.SUM)
+        ms, e2e_s, fwd_ms, bwd_ms = (float(x) for x in mx[:4])
+        total_comp = float(tot[4])
+    else:
+        total_comp = float(ncomp)
+    units_per_step = total_comp * T
+    value = units_per_step * args.steps / (ms / 1e3)
+    e2e_value = units_per_step * args.steps / e2e_s
+
+    if rank == 0:
+        peak, peak_src = _peaks()
+        fb, bb, tb = _alg_bytes(g)
+        achieved = bb * T / (bwd_ms / 1e3) / 1e9  # GB/s, backward kernel (dominant)
+        line = {
+            "metric": METRIC,
+            "value": value,
+            "unit": UNIT,
+            "n_gpus": ws,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": ms / args.steps,
+            "higher_is_better": True,
+            "scaling": "weak",
+            "vs_baseline": None,
+            "dtype": "f64",
+            "data": "synthetic",
+            "config": {
+                "workload": f"config2: {args.ncell} seeded random-tree cells per GPU (hh+pas, IClamp), "
+                            f"{T} steps dt 0.025 ms, soma-MSE vs lognormal teacher, forward + exact adjoint",
+                "compartments_per_gpu": ncomp,
+                "parallelism": f"cells sharded, {ws} GPU(s), no collective on the data path",
+                "l2": "tape (32 B/compartment-step, ~78 GB) exceeds L2; 256 MiB flush write between steps",
+                "loss": loss_val,
+            },
+            "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h)},
+            "gpu_launches": gpu_launches,
+            "fwd_ms": fwd_ms,
+            "bwd_ms": bwd_ms,
+            "roofline": {
+                "bound": "hbm",
+                "kernel": "bwd_kernel",
+                "achieved": achieved,
+                "peak": peak,
+                "peak_source": peak_src,
+                "unit": "GB/s",
+                "frac": achieved / peak,
+                "traffic": BWD_DRAM_BYTES_PER_UNIT * units_per_step / ws if BWD_DRAM_BYTES_PER_UNIT else None,
+                "alg_bytes_per_launch": bb * T,
+                "fwd_frac": (fb * T / (fwd_ms / 1e3) / 1e9) / peak,
+                "path_frac": (tb * T / ((fwd_ms + bwd_ms) / 1e3) / 1e9) / peak,
+            },
+            "clocks": clocks,
+        }
+        if ws == 1 and not args.no_cpu:
+            procs = os.cpu_count() or 1
+            ns = 4 * max(procs, 8)
+            v, units, wall = cpu_baseline(ns, T, procs)
+            line["cpu_baseline"] = {"value": v, "unit": UNIT, "cores": procs, "kind": "port",
+                                    "sample": f"{ns} cells of the config-2 batch, {T} steps, "
+                                              f"oracle forward + adjoint, {wall:.1f} s wall"}
+        print(json.dumps(line), flush=True)
+    s.close()
+    if dist:
+        dist.destroy_process_group()
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=("ours", "reference"))
+    ap.add_argument("--ncell", type=int, default=NCELL)
+    ap.add_argument("--nstep", type=int, default=T_STEPS)
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU-baseline leg")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        return run_reference(args)
+    return run_ours(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

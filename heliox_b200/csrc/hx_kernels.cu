@@ -585,6 +585,52 @@ __global__ void reduce_cols_kernel(const double* __restrict__ grad, const int* _
     out[c] = (float)s;
 }
 
+// Soma-trace MSE objective: loss = mean over rows 1..nrow-1 and all columns of
+// (trace - target)^2, dLdv = its gradient (row 0, the initial state, gets 0).
+// Deterministic: fixed-size block partials, then one block sums them in order.
+constexpr int kMseBlocks = 256;
+__global__ void mse_grad_kernel(const double* __restrict__ tr, const double* __restrict__ tg, double* __restrict__ g,
+                                double* __restrict__ partial, long long n, long long ncol, double scale) {
+    __shared__ double red[256];
+    double acc = 0.0;
+    for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
+        if (i < ncol) {
+            g[i] = 0.0;
+        } else {
+            const double e = tr[i] - tg[i];
+            g[i] = 2.0 * scale * e;
+            acc += e * e;
+        }
+    }
+    red[threadIdx.x] = acc;
+    __syncthreads();
+    for (int s = blockDim.x / 2; s > 0; s >>= 1) {
+        if ((int)threadIdx.x < s) red[threadIdx.x] += red[threadIdx.x + s];
+        __syncthreads();
+    }
+    if (threadIdx.x == 0) partial[blockIdx.x] = red[0];
+}
+
+__global__ void mse_final_kernel(const double* __restrict__ partial, double* __restrict__ loss, double scale) {
+    __shared__ double red[kMseBlocks];
+    red[threadIdx.x] = partial[threadIdx.x];
+    __syncthreads();
+    for (int s = kMseBlocks / 2; s > 0; s >>= 1) {
+        if ((int)threadIdx.x < s) red[threadIdx.x] += red[threadIdx.x + s];
+        __syncthreads();
+    }
+    if (threadIdx.x == 0) *loss = red[0] * scale;
+}
+
+cudaError_t launch_mse(const double* trace, const double* target, double* dLdv, double* partial, double* loss,
+                       int nrow, int ncol, cudaStream_t st) {
+    const long long n = (long long)nrow * ncol;
+    const double scale = (nrow > 1 && ncol > 0) ? 1.0 / ((double)(nrow - 1) * ncol) : 0.0;
+    mse_grad_kernel<<<kMseBlocks, 256, 0, st>>>(trace, target, dLdv, partial, n, ncol, scale);
+    mse_final_kernel<<<1, kMseBlocks, 0, st>>>(partial, loss, scale);
+    return cudaGetLastError();
+}
+
 // ------------------------------------------------------------------ launchers
 static size_t meta_bytes(const DevGroup& G) {
     return sizeof(int) * (3 * (size_t)G.smem_n + 1 + G.smem_nch + 4 * (size_t)G.smem_br + 1 + G.smem_bch + G.smem_lvl);

@@ -17,6 +17,9 @@ cudaError_t launch_bwd(const DevGroup& G, const DevTape& T, const DevAdj& A, con
                        const double* dLdv, const double* tmid, int k_hi, int k_lo, cudaStream_t st);
 cudaError_t launch_gather(const double* src, const int* idx, double* dst, int n, cudaStream_t st);
 cudaError_t launch_scatter(const double* src, const int* idx, double* dst, int n, cudaStream_t st);
+constexpr int kMsePartials = 256;
+cudaError_t launch_mse(const double* trace, const double* target, double* dLdv, double* partial, double* loss,
+                       int nrow, int ncol, cudaStream_t st);
 cudaError_t launch_reduce_cols(const double* grad, const int* col_off, const int* flat, const float* scale,
                                float* out, int ncol, cudaStream_t st);
 

@@ -95,10 +95,12 @@ struct hx_ctx {
     DevBuf<double> grad;  // concatenated per kind
     size_t grad_off[HX_P_COUNT + 1] = {0};
     DevBuf<double> tmid;
+    int tmid_steps = -1;
     DevBuf<int> pr_off, pr_local, pr_slot;
     std::vector<int> probe_key;
     int nprobe = 0;
     DevBuf<double> trace_dev, dLdv_dev, stage_dev;
+    DevBuf<double> mse_partial;
     DevBuf<int> red_off, red_flat;
     DevBuf<float> red_scale, red_out;
     PinBuf pin;
@@ -544,6 +546,7 @@ static hx::DevProbe probe_view(hx_ctx* c) {
 static int setup_time(hx_ctx* ctx, int nstep) {
     // t accumulates in half steps exactly as Simulate::fadvance_cpu does
     // (simulate.cpp:417 and :774); IClamp sees the mid-step value.
+    if (ctx->tmid_steps == nstep && ctx->tmid.p) return 0;
     std::vector<double> tm(std::max(nstep, 1));
     double t = 0.0;
     for (int k = 0; k < nstep; k++) {
@@ -552,6 +555,8 @@ static int setup_time(hx_ctx* ctx, int nstep) {
         t += 0.5 * ctx->dt;
     }
     HXC(ctx->tmid.upload(tm, ctx->st));
+    HXC(cudaStreamSynchronize(ctx->st));  // the source vector is pageable and goes out of scope
+    ctx->tmid_steps = nstep;
     return 0;
 }
 
@@ -777,6 +782,16 @@ int hx_reduce_grads_f32(hx_ctx* ctx, int n, const int* kind, const int* index, c
                                ctx->st));
     if (n_out) HXC(cudaMemcpyAsync(out, ctx->red_out.p, (size_t)n_out * 4, cudaMemcpyDeviceToHost, ctx->st));
     HXC(cudaStreamSynchronize(ctx->st));
+    return 0;
+}
+
+int hx_mse_loss_grad_dev(hx_ctx* ctx, const double* trace_dev, const double* target_dev, int nrow, int ncol,
+                         double* dLdv_dev, double* loss_dev) {
+    if (!ctx || !trace_dev || !target_dev || !dLdv_dev || !loss_dev || nrow < 1 || ncol < 0)
+        return fail(ctx, "bad argument");
+    HXC(cudaSetDevice(ctx->device));
+    HXC(ctx->mse_partial.ensure(hx::kMsePartials));
+    HXC(hx::launch_mse(trace_dev, target_dev, dLdv_dev, ctx->mse_partial.p, loss_dev, nrow, ncol, ctx->st));
     return 0;
 }
 

@@ -202,6 +202,27 @@ class Sim:
                                         _lib.fptr(scale), _lib.fptr(out), int(n_out)), "hx_reduce_grads_f32")
         return out
 
+    # ------------------------------------------------------------------ device-pointer variants
+    def forward_capture_dev(self, nstep: int, trace_ptr: int, v_init: Optional[float] = None, probes=None):
+        """Forward + tape with the probe trace written to a device buffer ((nstep+1) x nprobe doubles)."""
+        p = self._probe_arr(probes)
+        vi = self.group.v_init if v_init is None else v_init
+        self._check(self._L.hx_forward_capture_dev(self._ctx, int(nstep), float(vi), int(p.shape[0]), _lib.iptr(p),
+                                                   C.c_void_p(int(trace_ptr))), "hx_forward_capture_dev")
+        self._nstep, self._probes = int(nstep), p
+
+    def backward_dev(self, dLdv_ptr: int, grad_ptrs: Dict[str, int]):
+        """Adjoint of the last capture; dL/dv and the per-kind gradients are device buffers."""
+        arr = (C.c_void_p * _lib.HX_P_COUNT)()
+        for k, ptr in grad_ptrs.items():
+            arr[_lib.HX_P[k]] = C.c_void_p(int(ptr))
+        self._check(self._L.hx_backward_dev(self._ctx, C.c_void_p(int(dLdv_ptr)), arr), "hx_backward_dev")
+
+    def mse_loss_grad_dev(self, trace_ptr: int, target_ptr: int, nrow: int, ncol: int, dLdv_ptr: int, loss_ptr: int):
+        self._check(self._L.hx_mse_loss_grad_dev(self._ctx, C.c_void_p(int(trace_ptr)), C.c_void_p(int(target_ptr)),
+                                                 int(nrow), int(ncol), C.c_void_p(int(dLdv_ptr)),
+                                                 C.c_void_p(int(loss_ptr))), "hx_mse_loss_grad_dev")
+
     def last_kernel_ms(self, which: int):
         ms = C.c_double()
         n = C.c_int()

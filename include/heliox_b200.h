@@ -140,6 +140,16 @@ int hx_backward_dev(hx_ctx* ctx, const double* dLdv_dev, double* const* grads_de
 int hx_reduce_grads_f32(hx_ctx* ctx, int n, const int* kind, const int* index, const int32_t* dest,
                         const float* scale, float* out, int n_out);
 
+/* ---- objective -------------------------------------------------------------------- */
+/* Mean squared error of a probe trace against a target trace ((nrow x ncol),
+ * rows 1..nrow-1 count; row 0 is the initial state) and its gradient
+ * dLdv = 2 (trace - target) / ((nrow-1) ncol), row 0 = 0.  All device pointers;
+ * *loss_dev receives the loss.  Deterministic reduction.  The device-side
+ * counterpart of the Python objectives the reference's trainer evaluates
+ * (python_lib/heliox_learn/objective.py:15-30). */
+int hx_mse_loss_grad_dev(hx_ctx* ctx, const double* trace_dev, const double* target_dev, int nrow, int ncol,
+                         double* dLdv_dev, double* loss_dev);
+
 /* ---- timing (CUDA events on the launch stream) ---------------------------------- */
 /* Milliseconds of the last forward-capture / backward kernel work, measured with
  * events recorded around the launches.  which: 0 forward, 1 backward. */

@@ -64,6 +64,14 @@ class _Grads(C.Structure):
     ]
 
 
+REF_LIB = os.path.join(_HERE, "_ref", "libhxref.so")
+
+
+def ref_available() -> bool:
+    """True when the reference's own CPU integrator was compiled into oracle/_ref."""
+    return os.path.exists(REF_LIB)
+
+
 def build() -> str:
     """Compile the oracle (make) and return the .so path."""
     subprocess.run(["make", "-s", "-C", _HERE], check=True)
