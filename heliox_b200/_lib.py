@@ -99,6 +99,8 @@ SIGNATURES = {
     "hx_backward_dev": (C.c_int, [C.c_void_p, C.c_void_p, C.POINTER(C.c_void_p)]),
     "hx_reduce_grads_f32": (C.c_int, [C.c_void_p, C.c_int, _ip, _ip, _ip, _fp, _fp, C.c_int]),
     "hx_mse_loss_grad_dev": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_void_p, C.c_void_p]),
+    "hx_mse_loss_grad_noalloc": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_void_p, C.c_void_p,
+                                            C.c_void_p]),
     "hx_last_kernel_ms": (C.c_int, [C.c_void_p, C.c_int, _dp, _ip]),
 }
 

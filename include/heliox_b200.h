@@ -150,6 +150,22 @@ int hx_reduce_grads_f32(hx_ctx* ctx, int n, const int* kind, const int* index, c
 int hx_mse_loss_grad_dev(hx_ctx* ctx, const double* trace_dev, const double* target_dev, int nrow, int ncol,
                          double* dLdv_dev, double* loss_dev);
 
+/* The same loss and gradient as hx_mse_loss_grad_dev for callers that cannot
+ * let the library allocate device memory (a host that owns every device byte
+ * through its own pool, or a loop that must not meet cudaFree's implicit
+ * synchronisation).  No context and no allocation: the per-chunk partial sums
+ * live in a static device array of 4,096 doubles (32 KiB per device, held until
+ * the process exits), so nrow*ncol may be at most 4,096 * 65,536 = 2^28
+ * elements; larger inputs return -2 (with a message on stderr) and do no work.
+ * Work is enqueued on `stream` (NULL = the legacy default stream) of the
+ * current device.  The first call on a device resolves the scratch array's
+ * device address; make that first call before any stream capture.  All calls
+ * on a device share the array: calls that overlap on the GPU race.  Returns 0,
+ * -1 bad argument, -2 size beyond the maximum, -3 CUDA error.  It has no
+ * counterpart in the reference. */
+int hx_mse_loss_grad_noalloc(const double* trace_dev, const double* target_dev, int nrow, int ncol, double* dLdv_dev,
+                             double* loss_dev, void* stream);
+
 /* ---- timing (CUDA events on the launch stream) ---------------------------------- */
 /* Milliseconds of the last forward-capture / backward kernel work, measured with
  * events recorded around the launches.  which: 0 forward, 1 backward. */
