@@ -123,7 +123,15 @@ def _dist():
 
 # ----------------------------------------------------------------------------- CPU baseline
 def _cpu_cell_job(args):
-    seed, nstep = args
+    """One cell on one host core: forward + adjoint, returns (units, seconds).
+
+    With the reference harness built (oracle/_ref), the forward is the
+    reference's own CPU integrator (its CoreNEURON loader, Simulate::fadvance);
+    the reverse sweep -- which the reference does not have -- is the oracle's,
+    timed as (oracle forward + adjoint) - (oracle forward).  Otherwise both
+    halves are the oracle port.
+    """
+    seed, nstep, use_ref = args
     sys.path.insert(0, ROOT)
     import numpy as np
 
@@ -133,30 +141,38 @@ def _cpu_cell_job(args):
     g = synth.random_tree_cell(seed)
     t0 = time.perf_counter()
     tr, _ = O.forward(g, nstep)
+    t_fwd_port = time.perf_counter() - t0
     dLdv = np.zeros_like(tr)
     dLdv[1:] = 2.0 * tr[1:] / nstep
+    t0 = time.perf_counter()
     O.adjoint(g, nstep, dLdv)
-    return g.nnode * nstep, time.perf_counter() - t0
+    t_adj = time.perf_counter() - t0
+    t_bwd = max(t_adj - t_fwd_port, 0.0)
+    if use_ref:
+        t0 = time.perf_counter()
+        O.ref_forward(g, nstep)
+        t_fwd = time.perf_counter() - t0
+    else:
+        t_fwd = t_fwd_port
+    return g.nnode * nstep, t_fwd + t_bwd
 
 
 def cpu_baseline(ncell_sample: int, nstep: int, procs: int):
-    """Oracle forward + adjoint on host cores; spawn pool (no CUDA in the workers)."""
+    """Forward + adjoint of a cell sample on host cores; spawn pool (no CUDA in
+    the workers).  Returns (units per second over all cores, units, summed
+    per-core seconds / cores, kind)."""
     import multiprocessing as mp
 
-    ctx = mp.get_context("spawn")
-    jobs = [(SEED0 + c, nstep) for c in range(ncell_sample)]
-    t0 = time.perf_counter()
-    with ctx.Pool(procs) as pool:
-        res = pool.map(_cpu_cell_job, jobs)
-    wall = time.perf_counter() - t0
-    units = sum(r[0] for r in res)
-    return units / wall, units, wall
-
-
-def _ref_kind():
     from oracle import oracle as O
 
-    return "reference" if O.ref_available() else "port"
+    use_ref = O.ref_available()
+    ctx = mp.get_context("spawn")
+    jobs = [(SEED0 + c, nstep, use_ref) for c in range(ncell_sample)]
+    with ctx.Pool(procs) as pool:
+        res = pool.map(_cpu_cell_job, jobs)
+    units = sum(r[0] for r in res)
+    busy = sum(r[1] for r in res) / procs  # all cores busy in parallel
+    return units / busy, units, busy, ("reference" if use_ref else "port")
 
 
 # ----------------------------------------------------------------------------- reference arm
@@ -165,11 +181,11 @@ def run_reference(args):
     if rank != 0:
         return 0
     procs = os.cpu_count() or 1
-    kind = _ref_kind()
     vals = []
     sample = 2 * max(procs, 8)
+    kind = "port"
     for it in range(args.warmup + args.steps):
-        v, units, wall = cpu_baseline(sample, T_STEPS, procs)
+        v, units, wall, kind = cpu_baseline(sample, T_STEPS, procs)
         if it >= args.warmup:
             vals.append(v)
     value = statistics.median(vals)
@@ -189,7 +205,9 @@ def run_reference(args):
         "config": {"workload": f"config2: {NCELL} random-tree cells x {T_STEPS} steps, fwd+bwd",
                    "sample": f"{sample} cells x {T_STEPS} steps per step"},
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": procs, "kind": kind,
-                         "sample": f"{sample} cells of the config-2 batch, {T_STEPS} steps, forward + adjoint"},
+                         "sample": f"{sample} cells of the config-2 batch, {T_STEPS} steps; forward: "
+                                   + ("the reference's CPU integrator" if kind == "reference" else "oracle port")
+                                   + ", adjoint: oracle port (the reference has none)"},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -377,10 +395,11 @@ def run_ours(args):
         if ws == 1 and not args.no_cpu:
             procs = os.cpu_count() or 1
             ns = 4 * max(procs, 8)
-            v, units, wall = cpu_baseline(ns, T, procs)
-            line["cpu_baseline"] = {"value": v, "unit": UNIT, "cores": procs, "kind": "port",
-                                    "sample": f"{ns} cells of the config-2 batch, {T} steps, "
-                                              f"oracle forward + adjoint, {wall:.1f} s wall"}
+            v, units, wall, kind = cpu_baseline(ns, T, procs)
+            fwd_by = "the reference's CPU integrator" if kind == "reference" else "oracle port"
+            line["cpu_baseline"] = {"value": v, "unit": UNIT, "cores": procs, "kind": kind,
+                                    "sample": f"{ns} cells of the config-2 batch, {T} steps; forward: {fwd_by}, "
+                                              f"adjoint: oracle port; {wall:.1f} s per core"}
         print(json.dumps(line), flush=True)
     s.close()
     if dist:

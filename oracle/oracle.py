@@ -64,12 +64,53 @@ class _Grads(C.Structure):
     ]
 
 
-REF_LIB = os.path.join(_HERE, "_ref", "libhxref.so")
+REF_LIB = os.path.join(_HERE, "_ref", "hxref_run")
 
 
 def ref_available() -> bool:
     """True when the reference's own CPU integrator was compiled into oracle/_ref."""
     return os.path.exists(REF_LIB)
+
+
+def ref_forward(g, nstep: int, probe: Optional[Sequence[int]] = None, v_init: Optional[float] = None,
+                workdir: Optional[str] = None):
+    """Run the reference's own CPU integrator (oracle/_ref/hxref_run) on ``g``.
+
+    The group is exported in CoreNEURON format (heliox_b200.coredat) and loaded
+    by the reference's read_coredat/data_format_trans; returns
+    (trace[(nstep+1), nprobe], spikes list of (t, gid)).
+    """
+    import shutil
+    import tempfile
+
+    from heliox_b200.coredat import write_coredat
+
+    if not ref_available():
+        raise RuntimeError("reference harness not built (oracle/ref_build.sh)")
+    probe = np.ascontiguousarray(g.soma_nodes() if probe is None else probe, dtype=np.int32)
+    tmp = tempfile.mkdtemp(prefix="hxref_", dir=workdir)
+    try:
+        data = os.path.join(tmp, "data")
+        write_coredat(g, data)
+        pf = os.path.join(tmp, "probes.i32")
+        probe.tofile(pf)
+        tf = os.path.join(tmp, "trace.f64")
+        spk = os.path.join(tmp, "spk")
+        vi = float(g.v_init if v_init is None else v_init)
+        r = subprocess.run([REF_LIB, data, "0", repr(float(g.dt)), str(int(nstep)), repr(vi), pf, tf, spk],
+                           capture_output=True, text=True)
+        if r.returncode != 0:
+            raise RuntimeError(f"reference run failed ({r.returncode}):\n{r.stdout[-2000:]}\n{r.stderr[-2000:]}")
+        trace = np.fromfile(tf, dtype=np.float64).reshape(nstep + 1, probe.shape[0])
+        spikes = []
+        sf = os.path.join(spk, "spk.dat")
+        if os.path.exists(sf):
+            for line in open(sf):
+                t, gid = line.split()
+                spikes.append((float(t), int(gid)))
+        return trace, spikes
+    finally:
+        shutil.rmtree(tmp, ignore_errors=True)
 
 
 def build() -> str:

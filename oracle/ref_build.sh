@@ -1,0 +1,50 @@
+#!/usr/bin/env bash
+# Compiles the reference's own CPU integrator from its sources (read-only,
+# under the reference tree) into oracle/_ref/hxref_run -- TEST INFRASTRUCTURE
+# ONLY (the checker that pins oracle/hx_oracle.c).  No reference file is copied;
+# only the HighFive type shim (oracle/ref_shim) and the harness
+# (oracle/ref_harness.cpp) are ours.  Flags follow the reference's
+# CMakeLists.txt:7-31 (C++20, -ffp-contract=off, -fno-fast-math).
+set -euo pipefail
+REF=${HX_REFERENCE:-/root/reference}/src
+HERE=$(cd "$(dirname "$0")" && pwd)
+OUT=$HERE/_ref
+OBJ=$OUT/obj
+mkdir -p "$OBJ"
+if [ ! -d "$REF" ]; then echo "reference sources not found: $REF" >&2; exit 1; fi
+
+INC="-I$HERE/ref_shim -I/usr/local/cuda/include -I$REF -I$REF/io -I$REF/mech -I$REF/mech/build-in-mech -I$REF/mech/user-mech \
+ -I$REF/mech/worm-mech -I$REF/mech/worm-lr-mech -I$REF/utils -I$REF/spike -I$REF/spike/postsyn_mech \
+ -I$REF/spike/user_postsyn_mech -I$REF/third_party/CXXOPTS -I$REF/third_party/magic_enum -I$REF/third_party/Random123"
+CXXFLAGS="-std=c++20 -O2 -fPIC -ffp-contract=off -fno-fast-math -fexcess-precision=standard -w"
+NVFLAGS="-std=c++20 -O2 -Xcompiler -fPIC,-ffp-contract=off,-fno-fast-math,-w -diag-suppress=20040,177,550,186 -w \
+ -gencode arch=compute_100a,code=sm_100a"
+
+# the integrator, its loader and the mechanisms the synthetic configurations use
+SRCS=$(cd "$REF" && ls \
+  simulate.cpp simulate.cu neuron.cpp permute.cpp permute_order.cpp vecplay.cu \
+  io/*.cpp io/*.cu utils/*.cpp utils/*.cu mech/*.cpp mech/*.cu mech/build-in-mech/*.cpp mech/build-in-mech/*.cu \
+  spike/*.cpp spike/*.cu spike/postsyn_mech/*.cpp spike/postsyn_mech/*.cu optimizer/*.cpp optimizer/*.cu \
+  mech/user-mech/hh_templated.cu mech/user-mech/pas_templated.cu mech/user-mech/iclamp_templated.cu \
+  mech/user-mech/HalfGap.cu mech/worm-lr-mech/gapjunction_lr.cu mech/worm-lr-mech/neuron_to_neuron_syn_lr.cu \
+  2>/dev/null)
+
+compile() {
+  src=$1
+  obj=$OBJ/$(echo "$src" | tr '/' '_').o
+  if [ -f "$obj" ] && [ "$obj" -nt "$REF/$src" ]; then return 0; fi
+  case "$src" in
+    *.cu) nvcc $NVFLAGS $INC -c "$REF/$src" -o "$obj" ;;
+    *) g++ $CXXFLAGS $INC -c "$REF/$src" -o "$obj" ;;
+  esac
+}
+export -f compile
+export REF OBJ INC CXXFLAGS NVFLAGS
+echo "$SRCS" | xargs -P "$(nproc)" -I{} bash -c 'compile {}'
+
+g++ $CXXFLAGS $INC -c "$HERE/ref_harness.cpp" -o "$OBJ/_harness.o"
+g++ $CXXFLAGS -I/usr/local/cuda/include -c "$HERE/ref_nodev.cpp" -o "$OBJ/_nodev.o"
+# shared CUDA runtime, so that the host-only definitions in _nodev.o take precedence
+nvcc -gencode arch=compute_100a,code=sm_100a -o "$OUT/hxref_run" "$OBJ"/*.o -cudart shared -lpthread \
+  -Xlinker -rpath=/usr/local/cuda/lib64
+echo "built $OUT/hxref_run"

@@ -1,0 +1,44 @@
+"""Regenerates the golden fixtures from the reference's own CPU integrator.
+
+Needs the reference sources (to build oracle/_ref/hxref_run with
+oracle/ref_build.sh); run from the repository root:
+
+    python tests/golden/make_golden.py
+
+Each case exports a seeded synthetic group in CoreNEURON format
+(heliox_b200.coredat), runs the reference (read_coredat -> data_format_trans ->
+Simulate(CPU) finitialize + fadvance) and stores the voltage trace at the
+probes together with the spike list the reference writes (spk.dat).
+"""
+import os
+import sys
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+ROOT = os.path.dirname(os.path.dirname(HERE))
+sys.path.insert(0, ROOT)
+
+from heliox_b200 import synth  # noqa: E402
+from oracle import oracle as O  # noqa: E402
+
+CASES = {
+    "ball_and_stick": (lambda: synth.ball_and_stick(), 4000, [0, 1, 25, 50, 100]),
+    "ball_and_stick_teacher": (lambda: synth.ball_and_stick(gnabar_scale=1.1), 4000, [0]),
+    "trees3": (lambda: synth.random_tree_batch(3, seed0=20240), 4000, None),
+    "tree_deep": (lambda: synth.random_tree_cell(77, ncomp=400, max_levels=40), 2000, None),
+}
+
+
+def main():
+    for name, (make, nstep, probes) in CASES.items():
+        g = make()
+        p = np.asarray(probes if probes is not None else list(g.soma_nodes()) + [g.nnode - 1], dtype=np.int32)
+        tr, spk = O.ref_forward(g, nstep, probe=p)
+        np.savez_compressed(os.path.join(HERE, f"{name}.npz"), trace=tr, probes=p, nstep=nstep,
+                            spikes=np.asarray(spk, dtype=np.float64).reshape(-1, 2))
+        print(name, tr.shape, len(spk))
+
+
+if __name__ == "__main__":
+    main()
