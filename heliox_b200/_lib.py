@@ -102,6 +102,15 @@ SIGNATURES = {
     "hx_mse_loss_grad_noalloc": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_void_p, C.c_void_p,
                                             C.c_void_p]),
     "hx_last_kernel_ms": (C.c_int, [C.c_void_p, C.c_int, _dp, _ip]),
+    "hx_opt_create_adam": (C.c_int, [C.c_void_p, C.c_double, C.c_double, C.c_double]),
+    "hx_opt_add_params": (C.c_int, [C.c_void_p, C.c_int, C.c_int, _ip, _ip, C.c_double]),
+    "hx_opt_set_grads_f32": (C.c_int, [C.c_void_p, C.c_int, _fp, C.c_int]),
+    "hx_opt_grads_from_backward": (C.c_int, [C.c_void_p, C.c_int, C.c_double]),
+    "hx_opt_grad_buffer": (C.c_int, [C.c_void_p, C.c_int, C.POINTER(C.c_void_p), _ip]),
+    "hx_opt_step": (C.c_int, [C.c_void_p, C.c_int, C.c_double, C.c_double]),
+    "hx_opt_get_adam_state": (C.c_int, [C.c_void_p, C.c_int, C.POINTER(C.c_longlong), _dp, _dp, C.c_int, _dp]),
+    "hx_opt_set_adam_state": (C.c_int, [C.c_void_p, C.c_int, C.c_longlong, _dp, _dp, C.c_int, _dp]),
+    "hx_opt_reset": (C.c_int, [C.c_void_p, C.c_int]),
 }
 
 _LIB = None

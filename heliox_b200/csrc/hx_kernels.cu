@@ -631,6 +631,62 @@ cudaError_t launch_mse(const double* trace, const double* target, double* dLdv, 
     return cudaGetLastError();
 }
 
+// Adam over external-gradient slots, one slot per registered parameter
+// (reference: AdamOptimizer::step_cpu, src/optimizer/optimizer.cpp:351-397, with
+// one weight per entry): g = grad*impedance*inv_record_steps, biased moments,
+// bias correction with the host-computed powers, w -= lr*mhat/(sqrt(vhat)+eps),
+// then the gradient slot is zeroed.
+__global__ void adam_kernel(double* const* __restrict__ wbase, const int* __restrict__ kind,
+                            const int* __restrict__ slot, double* __restrict__ grad, double* __restrict__ m,
+                            double* __restrict__ v, int n, double lr, double impedance, double inv_record_steps,
+                            double beta1, double beta2, double eps, double bc1, double bc2) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    const double g = grad[i] * impedance * inv_record_steps;
+    const double mi = beta1 * m[i] + (1.0 - beta1) * g;
+    const double vi = beta2 * v[i] + (1.0 - beta2) * g * g;
+    m[i] = mi;
+    v[i] = vi;
+    const double mh = mi / (1.0 - bc1);
+    const double vh = vi / (1.0 - bc2);
+    double* w = wbase[kind[i]] + slot[i];
+    *w = *w - lr * mh / (sqrt(vh) + eps);
+    grad[i] = 0.0;
+}
+
+cudaError_t launch_adam(double* const* wbase, const int* kind, const int* slot, double* grad, double* m, double* v,
+                        int n, double lr, double impedance, double inv_record_steps, double beta1, double beta2,
+                        double eps, double bc1, double bc2, cudaStream_t st) {
+    if (n <= 0) return cudaSuccess;
+    adam_kernel<<<(n + 255) / 256, 256, 0, st>>>(wbase, kind, slot, grad, m, v, n, lr, impedance, inv_record_steps,
+                                                 beta1, beta2, eps, bc1, bc2);
+    return cudaGetLastError();
+}
+
+// grad[i] = src[flat[i]] * scale (adjoint gradients into optimizer slots)
+__global__ void take_scaled_kernel(const double* __restrict__ src, const int* __restrict__ flat,
+                                   double* __restrict__ dst, int n, double scale) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < n) dst[i] = src[flat[i]] * scale;
+}
+
+cudaError_t launch_take_scaled(const double* src, const int* flat, double* dst, int n, double scale, cudaStream_t st) {
+    if (n <= 0) return cudaSuccess;
+    take_scaled_kernel<<<(n + 255) / 256, 256, 0, st>>>(src, flat, dst, n, scale);
+    return cudaGetLastError();
+}
+
+__global__ void f32_to_f64_kernel(const float* __restrict__ a, double* __restrict__ b, int n) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < n) b[i] = (double)a[i];
+}
+
+cudaError_t launch_f32_to_f64(const float* a, double* b, int n, cudaStream_t st) {
+    if (n <= 0) return cudaSuccess;
+    f32_to_f64_kernel<<<(n + 255) / 256, 256, 0, st>>>(a, b, n);
+    return cudaGetLastError();
+}
+
 // ------------------------------------------------------------------ launchers
 static size_t meta_bytes(const DevGroup& G) {
     return sizeof(int) * (3 * (size_t)G.smem_n + 1 + G.smem_nch + 4 * (size_t)G.smem_br + 1 + G.smem_bch + G.smem_lvl);

@@ -20,6 +20,11 @@ cudaError_t launch_scatter(const double* src, const int* idx, double* dst, int n
 constexpr int kMsePartials = 256;
 cudaError_t launch_mse(const double* trace, const double* target, double* dLdv, double* partial, double* loss,
                        int nrow, int ncol, cudaStream_t st);
+cudaError_t launch_adam(double* const* wbase, const int* kind, const int* slot, double* grad, double* m, double* v,
+                        int n, double lr, double impedance, double inv_record_steps, double beta1, double beta2,
+                        double eps, double bc1, double bc2, cudaStream_t st);
+cudaError_t launch_take_scaled(const double* src, const int* flat, double* dst, int n, double scale, cudaStream_t st);
+cudaError_t launch_f32_to_f64(const float* a, double* b, int n, cudaStream_t st);
 cudaError_t launch_reduce_cols(const double* grad, const int* col_off, const int* flat, const float* scale,
                                float* out, int ncol, cudaStream_t st);
 

@@ -65,6 +65,17 @@ struct PinBuf {
 
 }  // namespace
 
+// Adam over external-gradient slots (one per registered parameter instance).
+struct AdamOpt {
+    double beta1 = 0.9, beta2 = 0.999, eps = 1e-8, impedance = 1.0;
+    long long step = 0;
+    int n = 0;
+    std::vector<int> kind_h, ref_h;
+    DevBuf<int> kind, slot, flat;
+    DevBuf<double> grad, m, v;
+    DevBuf<float> f32;
+};
+
 struct hx_ctx {
     int device = 0;
     cudaStream_t own = nullptr, st = nullptr;
@@ -109,6 +120,8 @@ struct hx_ctx {
     int nstep = 0;
     int seg = 0, nseg = 0;  // steps per segment (checkpoint interval) and count
     bool full_tape = true;
+    std::vector<AdamOpt*> opts;
+    DevBuf<double*> prm_ptrs;  // device copy of prm[kind].p
     cudaEvent_t ev[4] = {nullptr, nullptr, nullptr, nullptr};
     int launches[2] = {0, 0};
 };
@@ -200,6 +213,7 @@ int hx_destroy(hx_ctx* ctx) {
     for (auto& e : ctx->ev)
         if (e) cudaEventDestroy(e);
     if (ctx->own) cudaStreamDestroy(ctx->own);
+    for (AdamOpt* o : ctx->opts) delete o;
     delete ctx;
     return 0;
 }
@@ -454,6 +468,13 @@ int hx_load_group(hx_ctx* ctx, const hx_group_desc* desc) {
         return fail(ctx, "cell pack needs " + std::to_string(sb) + " B shared memory (> " + std::to_string(maxsmem) +
                              "); lower the pack target or split the cell");
     HXC(hx::configure_kernels(sf, sb));
+    {
+        std::vector<double*> ptrs(HX_P_COUNT);
+        for (int k = 0; k < HX_P_COUNT; k++) ptrs[k] = ctx->prm[k].p;
+        HXC(ctx->prm_ptrs.upload(ptrs, st));
+    }
+    for (AdamOpt* o : ctx->opts) delete o;  // bindings refer to the previous group
+    ctx->opts.clear();
     HXC(cudaStreamSynchronize(st));
     ctx->loaded = true;
     return 0;
@@ -802,6 +823,151 @@ int hx_last_kernel_ms(hx_ctx* ctx, int which, double* ms, int* launches) {
     HXC(cudaEventElapsedTime(&f, ctx->ev[which * 2], ctx->ev[which * 2 + 1]));
     if (ms) *ms = f;
     if (launches) *launches = ctx->launches[which];
+    return 0;
+}
+
+}  // extern "C"
+
+// ---------------------------------------------------------------- optimizer
+static AdamOpt* get_opt(hx_ctx* ctx, int id) {
+    if (!ctx || id < 0 || id >= (int)ctx->opts.size() || !ctx->opts[id]) return nullptr;
+    return ctx->opts[id];
+}
+
+extern "C" {
+
+int hx_opt_create_adam(hx_ctx* ctx, double beta1, double beta2, double eps) {
+    if (!ctx) return -1;
+    if (!ctx->loaded) return fail(ctx, "no group loaded");
+    if (!(beta1 >= 0 && beta1 < 1) || !(beta2 >= 0 && beta2 < 1) || !(eps > 0)) return fail(ctx, "bad Adam hyperparameters");
+    AdamOpt* o = new AdamOpt();
+    o->beta1 = beta1;
+    o->beta2 = beta2;
+    o->eps = eps;
+    ctx->opts.push_back(o);
+    return (int)ctx->opts.size() - 1;
+}
+
+int hx_opt_add_params(hx_ctx* ctx, int opt, int n, const int* kind, const int* index, double impedance) {
+    AdamOpt* o = get_opt(ctx, opt);
+    if (!o) return fail(ctx, "bad optimizer id");
+    if (n <= 0 || !kind || !index) return fail(ctx, "empty parameter list");
+    if (!(impedance > 0)) return fail(ctx, "impedance must be positive");
+    HXC(cudaSetDevice(ctx->device));
+    std::vector<int> kv(n), sv(n), fv(n);
+    for (int i = 0; i < n; i++) {
+        if (kind[i] < 0 || kind[i] >= HX_P_COUNT) return fail(ctx, "bad parameter kind");
+        if (index[i] < 0 || (size_t)index[i] >= kind_count(ctx->P, kind[i])) return fail(ctx, "parameter index out of range");
+        kv[i] = kind[i];
+        sv[i] = ctx->kmap_h[kind[i]][index[i]];
+        fv[i] = (int)ctx->grad_off[kind[i]] + sv[i];
+    }
+    o->kind_h = kv;
+    o->ref_h.assign(index, index + n);
+    o->n = n;
+    o->impedance = impedance;
+    o->step = 0;
+    HXC(o->kind.upload(kv, ctx->st));
+    HXC(o->slot.upload(sv, ctx->st));
+    HXC(o->flat.upload(fv, ctx->st));
+    HXC(o->grad.ensure(n));
+    HXC(o->m.ensure(n));
+    HXC(o->v.ensure(n));
+    HXC(o->f32.ensure(n));
+    HXC(cudaMemsetAsync(o->grad.p, 0, n * 8, ctx->st));
+    HXC(cudaMemsetAsync(o->m.p, 0, n * 8, ctx->st));
+    HXC(cudaMemsetAsync(o->v.p, 0, n * 8, ctx->st));
+    HXC(cudaStreamSynchronize(ctx->st));
+    return 0;
+}
+
+int hx_opt_set_grads_f32(hx_ctx* ctx, int opt, const float* grads, int n) {
+    AdamOpt* o = get_opt(ctx, opt);
+    if (!o || !grads) return fail(ctx, "bad argument");
+    if (n != o->n) return fail(ctx, "gradient count mismatch");
+    HXC(cudaSetDevice(ctx->device));
+    HXC(cudaMemcpyAsync(o->f32.p, grads, (size_t)n * 4, cudaMemcpyHostToDevice, ctx->st));
+    HXC(hx::launch_f32_to_f64(o->f32.p, o->grad.p, n, ctx->st));
+    HXC(cudaStreamSynchronize(ctx->st));
+    return 0;
+}
+
+int hx_opt_grads_from_backward(hx_ctx* ctx, int opt, double scale) {
+    AdamOpt* o = get_opt(ctx, opt);
+    if (!o) return fail(ctx, "bad optimizer id");
+    if (!ctx->captured) return fail(ctx, "no backward to take gradients from");
+    HXC(cudaSetDevice(ctx->device));
+    HXC(hx::launch_take_scaled(ctx->grad.p, o->flat.p, o->grad.p, o->n, scale, ctx->st));
+    return 0;
+}
+
+int hx_opt_grad_buffer(hx_ctx* ctx, int opt, double** dev_ptr, int* n) {
+    AdamOpt* o = get_opt(ctx, opt);
+    if (!o || !dev_ptr || !n) return fail(ctx, "bad argument");
+    *dev_ptr = o->grad.p;
+    *n = o->n;
+    return 0;
+}
+
+int hx_opt_step(hx_ctx* ctx, int opt, double lr, double inv_record_steps) {
+    AdamOpt* o = get_opt(ctx, opt);
+    if (!o) return fail(ctx, "bad optimizer id");
+    HXC(cudaSetDevice(ctx->device));
+    o->step++;
+    const double bc1 = std::pow(o->beta1, (double)o->step);
+    const double bc2 = std::pow(o->beta2, (double)o->step);
+    HXC(hx::launch_adam(ctx->prm_ptrs.p, o->kind.p, o->slot.p, o->grad.p, o->m.p, o->v.p, o->n, lr,
+                        o->impedance, inv_record_steps, o->beta1, o->beta2, o->eps, bc1, bc2, ctx->st));
+    return 0;
+}
+
+int hx_opt_get_adam_state(hx_ctx* ctx, int opt, long long* step, double* m, double* v, int n, double* hyper3) {
+    AdamOpt* o = get_opt(ctx, opt);
+    if (!o) return fail(ctx, "bad optimizer id");
+    if (n != o->n) return fail(ctx, "state size mismatch");
+    HXC(cudaSetDevice(ctx->device));
+    if (step) *step = o->step;
+    if (m) HXC(cudaMemcpyAsync(m, o->m.p, (size_t)n * 8, cudaMemcpyDeviceToHost, ctx->st));
+    if (v) HXC(cudaMemcpyAsync(v, o->v.p, (size_t)n * 8, cudaMemcpyDeviceToHost, ctx->st));
+    HXC(cudaStreamSynchronize(ctx->st));
+    if (hyper3) {
+        hyper3[0] = o->beta1;
+        hyper3[1] = o->beta2;
+        hyper3[2] = o->eps;
+    }
+    return 0;
+}
+
+int hx_opt_set_adam_state(hx_ctx* ctx, int opt, long long step, const double* m, const double* v, int n,
+                          const double* hyper3) {
+    AdamOpt* o = get_opt(ctx, opt);
+    if (!o || !m || !v) return fail(ctx, "bad argument");
+    if (n != o->n) return fail(ctx, "state size mismatch");
+    if (step < 0) return fail(ctx, "negative step count");
+    HXC(cudaSetDevice(ctx->device));
+    o->step = step;
+    HXC(cudaMemcpyAsync(o->m.p, m, (size_t)n * 8, cudaMemcpyHostToDevice, ctx->st));
+    HXC(cudaMemcpyAsync(o->v.p, v, (size_t)n * 8, cudaMemcpyHostToDevice, ctx->st));
+    HXC(cudaStreamSynchronize(ctx->st));
+    if (hyper3) {
+        o->beta1 = hyper3[0];
+        o->beta2 = hyper3[1];
+        o->eps = hyper3[2];
+    }
+    return 0;
+}
+
+int hx_opt_reset(hx_ctx* ctx, int opt) {
+    AdamOpt* o = get_opt(ctx, opt);
+    if (!o) return fail(ctx, "bad optimizer id");
+    HXC(cudaSetDevice(ctx->device));
+    o->step = 0;
+    if (o->n) {
+        HXC(cudaMemsetAsync(o->m.p, 0, (size_t)o->n * 8, ctx->st));
+        HXC(cudaMemsetAsync(o->v.p, 0, (size_t)o->n * 8, ctx->st));
+        HXC(cudaMemsetAsync(o->grad.p, 0, (size_t)o->n * 8, ctx->st));
+    }
+    HXC(cudaStreamSynchronize(ctx->st));
     return 0;
 }
 

@@ -1,0 +1,190 @@
+"""``heliox_learn``-compatible surface for the exact adjoint.
+
+The reference's learning package defines a gradient-method plugin slot
+(``GradientMethod``: ``spec``, ``capture(runtime, state)``,
+``backward(runtime, captured, dL_dprobe)``, python_lib/heliox_learn/method.py:
+15-32), column mappings of runtime handles (``MappedSignal``, signals.py:9-37)
+and the result type ``ReplayGrads(dw_out_n, dx_lr_it)`` (signals.py:94-99).
+``AdjointMethod`` plugs the exact discrete adjoint into that slot: ``capture``
+runs the forward with tape, ``backward`` runs the reverse sweep and reduces the
+per-instance gradients into the N columns of a ``MappedSignal`` on the device
+(the reference's batch_scatter_add, src/runtime_api/core/kernels/
+batch_scatter_add.cu:4-27).  ``train_adam`` is the loop the reference drives
+through ``Sim.optimizer_*`` (SimWrapper.cpp:284-451), run on the device.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass, field
+from typing import Any, Callable, Dict, List, Optional, Protocol, Sequence, Tuple, runtime_checkable
+
+import numpy as np
+
+from .model import CellGroup
+from .runtime import Sim
+
+
+@dataclass(frozen=True)
+class MethodSpec:
+    name: str
+    precise: bool = True
+
+
+@runtime_checkable
+class GradientMethod(Protocol):
+    @property
+    def spec(self) -> MethodSpec: ...
+
+    def capture(self, runtime: Any, *, state: Any) -> Any: ...
+
+    def backward(self, runtime: Any, *, captured: Any, dL_dprobe: Any) -> Any: ...
+
+
+@dataclass(frozen=True)
+class MappedSignal:
+    """Handles gathered and scatter-added into N columns: out[dest[j]] += scale[j] * x[handles[j]]."""
+
+    name: str
+    handles: Sequence[int]
+    dest: np.ndarray  # int32 (len(handles),)
+    scale: np.ndarray  # float32 (len(handles),)
+
+    def __post_init__(self) -> None:
+        if self.dest.ndim != 1 or self.scale.ndim != 1:
+            raise ValueError(f"MappedSignal({self.name}): dest/scale must be 1D arrays")
+        if int(self.dest.shape[0]) != len(self.handles) or int(self.scale.shape[0]) != len(self.handles):
+            raise ValueError(f"MappedSignal({self.name}): size mismatch")
+        if self.dest.dtype != np.int32:
+            raise TypeError(f"MappedSignal({self.name}): dest must be int32 (got {self.dest.dtype})")
+        if self.scale.dtype != np.float32:
+            raise TypeError(f"MappedSignal({self.name}): scale must be float32 (got {self.scale.dtype})")
+
+    @property
+    def n_columns(self) -> int:
+        return int(self.dest.max()) + 1 if self.dest.size else 0
+
+
+@dataclass(frozen=True)
+class ReplayGrads:
+    dw_out_n: np.ndarray  # float32 (N,)
+    dx_lr_it: Optional[np.ndarray] = None
+
+
+@dataclass(frozen=True)
+class AdjointCaptureSpec:
+    """Forward capture: voltages at probe nodes over ``total_steps`` steps."""
+
+    probe_nodes: Sequence[int]
+    total_steps: int
+    v_init: Optional[float] = None
+
+
+@dataclass
+class CapturedTrace:
+    output_vs_tn: np.ndarray  # float64 (total_steps+1, n_output)
+
+    @property
+    def total_steps(self) -> int:
+        return int(self.output_vs_tn.shape[0]) - 1
+
+    @property
+    def n_output(self) -> int:
+        return int(self.output_vs_tn.shape[1])
+
+
+class AdjointRuntime:
+    """A loaded cell group on one GPU (the counterpart of heliox_learn.Runtime)."""
+
+    def __init__(self, group: CellGroup, device: int = 0, **sim_kwargs):
+        self.group = group
+        self.sim = Sim(device, **sim_kwargs)
+        self.sim.load_group(group)
+
+    @property
+    def loaded(self) -> bool:
+        return True
+
+    @property
+    def dt_ms(self) -> float:
+        return float(self.group.dt)
+
+    @property
+    def v_init(self) -> float:
+        return float(self.group.v_init)
+
+    def handle(self, mech: str, var: str, idx: int) -> int:
+        return self.sim.get_variable_handle(mech, var, idx)
+
+    def close(self) -> None:
+        self.sim.close()
+
+
+@dataclass
+class AdjointState:
+    spec: AdjointCaptureSpec
+    params: MappedSignal
+
+
+class AdjointMethod:
+    """Exact discrete adjoint in the GradientMethod slot."""
+
+    @property
+    def spec(self) -> MethodSpec:
+        return MethodSpec("adjoint", precise=True)
+
+    def capture(self, runtime: AdjointRuntime, *, state: AdjointState) -> CapturedTrace:
+        sp = state.spec
+        tr = runtime.sim.forward_capture(int(sp.total_steps), v_init=sp.v_init,
+                                         probes=np.asarray(sp.probe_nodes, dtype=np.int32))
+        return CapturedTrace(tr)
+
+    def backward(self, runtime: AdjointRuntime, *, captured: CapturedTrace, dL_dprobe: np.ndarray,
+                 state: Optional[AdjointState] = None) -> ReplayGrads:
+        if state is None:
+            raise ValueError("AdjointMethod.backward needs the state with the parameter mapping")
+        runtime.sim.backward(np.asarray(dL_dprobe, dtype=np.float64), keys=())
+        p = state.params
+        dw = runtime.sim.reduce_grads_f32(list(p.handles), p.dest, p.scale, p.n_columns)
+        return ReplayGrads(dw_out_n=dw, dx_lr_it=None)
+
+
+def mse_objective(trace: np.ndarray, target: np.ndarray) -> Tuple[float, np.ndarray]:
+    """Soma-voltage MSE over steps 1..T and its gradient dL/dtrace (row 0 is the initial state)."""
+    err = trace[1:] - target[1:]
+    n = err.size
+    loss = float(np.sum(err * err) / n)
+    g = np.zeros_like(trace)
+    g[1:] = (2.0 / n) * err
+    return loss, g
+
+
+def train_adam(runtime: AdjointRuntime, handles: Sequence[int], target: np.ndarray, epochs: int,
+               lr: float = 1e-3, probes: Optional[Sequence[int]] = None, total_steps: Optional[int] = None,
+               allreduce: Optional[Callable[[int, int], None]] = None,
+               on_epoch: Optional[Callable[[int, float], None]] = None) -> List[float]:
+    """Fit the parameters behind ``handles`` to ``target`` with the device Adam.
+
+    Each epoch: forward capture, MSE against ``target`` on the host, reverse
+    sweep, gradients of the bound parameters copied into the optimizer's slots
+    on the device (optionally all-reduced across ranks by ``allreduce(ptr, n)``),
+    one Adam step.  Returns the loss history.
+    """
+    sim = runtime.sim
+    probes = runtime.group.soma_nodes() if probes is None else np.asarray(probes, dtype=np.int32)
+    T = int(total_steps if total_steps is not None else target.shape[0] - 1)
+    opt = sim.create_optimizer("adam")
+    sim.optimizer_add_external_grads(opt, list(handles), impedance=1.0)
+    hist = []
+    for ep in range(int(epochs)):
+        tr = sim.forward_capture(T, probes=probes)
+        loss, g = mse_objective(tr, target)
+        sim.backward(g, keys=())
+        sim.optimizer_grads_from_backward(opt)
+        if allreduce is not None:
+            ptr, n = sim.optimizer_grad_buffer(opt)
+            allreduce(ptr, n)
+        sim.optimizer_step_with_inv_record_steps(opt, lr, 1.0)
+        hist.append(loss)
+        if on_epoch:
+            on_epoch(ep, loss)
+    sim.synchronize()
+    return hist

@@ -61,7 +61,7 @@ class Sim:
         self._bound = None
         self._nstep = None
         self._probes = None
-        self._optimizers: Dict[int, "_AdamOpt"] = {}
+        self._opt_hyper: Dict[int, tuple] = {}
 
     # ------------------------------------------------------------------ basics
     def _check(self, rc: int, what: str):
@@ -222,6 +222,91 @@ class Sim:
         self._check(self._L.hx_mse_loss_grad_dev(self._ctx, C.c_void_p(int(trace_ptr)), C.c_void_p(int(target_ptr)),
                                                  int(nrow), int(ncol), C.c_void_p(int(dLdv_ptr)),
                                                  C.c_void_p(int(loss_ptr))), "hx_mse_loss_grad_dev")
+
+    # ------------------------------------------------------------------ optimizer
+    # Mirrors Sim.create_optimizer / configure_optimizer / optimizer_add_external_grads /
+    # optimizer_set_external_grads_f32 / optimizer_step_with_inv_record_steps /
+    # optimizer_get/set_adam_state / optimizer_reset_state
+    # (src/python_api/PyBindings.cpp:43-65, SimWrapper.cpp:284-451).
+    def create_optimizer(self, kind: str = "adam", beta1: float = 0.9, beta2: float = 0.999,
+                         epsilon: float = 1e-8) -> int:
+        if kind.lower() != "adam":
+            raise HxError(f"optimizer {kind!r} is not provided (Adam is the training step of this path)")
+        oid = self._L.hx_opt_create_adam(self._ctx, float(beta1), float(beta2), float(epsilon))
+        if oid < 0:
+            self._check(oid, "hx_opt_create_adam")
+        self._opt_hyper[oid] = (float(beta1), float(beta2), float(epsilon))
+        return oid
+
+    def configure_optimizer(self, opt: int, momentum: float = 0.9, beta1: float = 0.9, beta2: float = 0.999,
+                            epsilon: float = 1e-8):
+        self._opt_hyper[opt] = (float(beta1), float(beta2), float(epsilon))
+        n = self._opt_n(opt)
+        if n:
+            step, m, v, _ = self.optimizer_get_adam_state(opt)
+            self.optimizer_set_adam_state(opt, step, m, v, beta1, beta2, epsilon)
+
+    def _opt_n(self, opt: int) -> int:
+        ptr = C.c_void_p()
+        n = C.c_int(0)
+        if self._L.hx_opt_grad_buffer(self._ctx, int(opt), C.byref(ptr), C.byref(n)) != 0:
+            return 0
+        return int(n.value)
+
+    def optimizer_add_external_grads(self, opt: int, weight_handles: Sequence[int], impedance: float = 1.0):
+        kinds = np.array([split_handle(h)[0] for h in weight_handles], dtype=np.int32)
+        idx = np.array([split_handle(h)[1] for h in weight_handles], dtype=np.int32)
+        self._check(self._L.hx_opt_add_params(self._ctx, int(opt), int(kinds.shape[0]), _lib.iptr(kinds),
+                                              _lib.iptr(idx), float(impedance)), "hx_opt_add_params")
+        b1, b2, eps = self._opt_hyper.get(opt, (0.9, 0.999, 1e-8))
+        n = int(kinds.shape[0])
+        self.optimizer_set_adam_state(opt, 0, np.zeros(n), np.zeros(n), b1, b2, eps)
+
+    def optimizer_set_external_grads_f32(self, opt: int, grads: np.ndarray):
+        g = np.ascontiguousarray(grads, dtype=np.float32)
+        self._check(self._L.hx_opt_set_grads_f32(self._ctx, int(opt), _lib.fptr(g), int(g.shape[0])),
+                    "hx_opt_set_grads_f32")
+
+    def optimizer_grads_from_backward(self, opt: int, scale: float = 1.0):
+        """Slot gradients := the last backward's gradients of the bound parameters (device, fp64)."""
+        self._check(self._L.hx_opt_grads_from_backward(self._ctx, int(opt), float(scale)), "hx_opt_grads_from_backward")
+
+    def optimizer_grad_buffer(self, opt: int):
+        """(device pointer, n) of the slot gradients, e.g. for an all-reduce across ranks."""
+        ptr = C.c_void_p()
+        n = C.c_int(0)
+        self._check(self._L.hx_opt_grad_buffer(self._ctx, int(opt), C.byref(ptr), C.byref(n)), "hx_opt_grad_buffer")
+        return int(ptr.value or 0), int(n.value)
+
+    def optimizer_step_with_inv_record_steps(self, opt: int, learning_rate: float, inv_record_steps: float = 1.0):
+        self._check(self._L.hx_opt_step(self._ctx, int(opt), float(learning_rate), float(inv_record_steps)),
+                    "hx_opt_step")
+
+    def optimizer_get_adam_state(self, opt: int):
+        n = self._opt_n(opt)
+        m = np.zeros(max(n, 1))
+        v = np.zeros(max(n, 1))
+        step = C.c_longlong(0)
+        hyper = np.zeros(3)
+        self._check(self._L.hx_opt_get_adam_state(self._ctx, int(opt), C.byref(step), _lib.dptr(m), _lib.dptr(v), n,
+                                                  _lib.dptr(hyper)), "hx_opt_get_adam_state")
+        return int(step.value), m[:n], v[:n], tuple(float(x) for x in hyper)
+
+    def optimizer_set_adam_state(self, opt: int, step: int, m, v, beta1: float = 0.9, beta2: float = 0.999,
+                                 epsilon: float = 1e-8):
+        m = np.ascontiguousarray(m, dtype=np.float64)
+        v = np.ascontiguousarray(v, dtype=np.float64)
+        hyper = np.array([beta1, beta2, epsilon], dtype=np.float64)
+        self._check(self._L.hx_opt_set_adam_state(self._ctx, int(opt), int(step), _lib.dptr(m), _lib.dptr(v),
+                                                  int(m.shape[0]), _lib.dptr(hyper)), "hx_opt_set_adam_state")
+        self._opt_hyper[opt] = (float(beta1), float(beta2), float(epsilon))
+
+    def optimizer_reset_state(self, opt: int):
+        self._check(self._L.hx_opt_reset(self._ctx, int(opt)), "hx_opt_reset")
+
+    def synchronize(self):
+        """Wait for the context's work (the optimizer step is asynchronous)."""
+        self.get_param_array("cm")
 
     def last_kernel_ms(self, which: int):
         ms = C.c_double()

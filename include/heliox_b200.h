@@ -140,6 +140,30 @@ int hx_backward_dev(hx_ctx* ctx, const double* dLdv_dev, double* const* grads_de
 int hx_reduce_grads_f32(hx_ctx* ctx, int n, const int* kind, const int* index, const int32_t* dest,
                         const float* scale, float* out, int n_out);
 
+/* ---- optimizer ---------------------------------------------------------------------- */
+/* Adam over parameter instances, updating the device parameters in place.
+ * Mirrors Simulate::create_optimizer / configure_optimizer /
+ * optimizer_step_with_inv_record_steps (src/simulate.cpp:1102-1280) and the
+ * external-gradient binding of SimWrapper (src/python_api/SimWrapper.cpp:
+ * 284-451): one slot per parameter, g = grad * impedance * inv_record_steps,
+ * bias-corrected moments (AdamOptimizer::step_cpu, src/optimizer/optimizer.cpp:
+ * 351-397), gradients zeroed after each step.  Returns an optimizer id >= 0. */
+int hx_opt_create_adam(hx_ctx* ctx, double beta1, double beta2, double eps);
+/* Binds n parameter instances (kind, reference index), replacing any previous binding. */
+int hx_opt_add_params(hx_ctx* ctx, int opt, int n, const int* kind, const int* index, double impedance);
+/* Host float32 gradients for the bound slots (optimizer_set_external_grads_f32). */
+int hx_opt_set_grads_f32(hx_ctx* ctx, int opt, const float* grads, int n);
+/* Device: slot gradients := the last backward's gradients of the bound instances times scale. */
+int hx_opt_grads_from_backward(hx_ctx* ctx, int opt, double scale);
+/* Device pointer and length of the slot gradients (e.g. for an all-reduce before hx_opt_step). */
+int hx_opt_grad_buffer(hx_ctx* ctx, int opt, double** dev_ptr, int* n);
+int hx_opt_step(hx_ctx* ctx, int opt, double lr, double inv_record_steps);
+/* hyper3 = {beta1, beta2, eps}; optimizer_get/set_adam_state (SimWrapper.cpp:419-451). */
+int hx_opt_get_adam_state(hx_ctx* ctx, int opt, long long* step, double* m, double* v, int n, double* hyper3);
+int hx_opt_set_adam_state(hx_ctx* ctx, int opt, long long step, const double* m, const double* v, int n,
+                          const double* hyper3);
+int hx_opt_reset(hx_ctx* ctx, int opt);
+
 /* ---- objective -------------------------------------------------------------------- */
 /* Mean squared error of a probe trace against a target trace ((nrow x ncol),
  * rows 1..nrow-1 count; row 0 is the initial state) and its gradient

@@ -113,6 +113,48 @@ def ref_forward(g, nstep: int, probe: Optional[Sequence[int]] = None, v_init: Op
         shutil.rmtree(tmp, ignore_errors=True)
 
 
+def adam_port(w0, grads, lr, inv_record_steps, beta1=0.9, beta2=0.999, eps=1e-8, impedance=1.0):
+    """Restatement of AdamOptimizer::step_cpu (src/optimizer/optimizer.cpp:351-397)
+    for one weight per entry, same operation order.  Returns (weights after each
+    step [steps, n], m, v)."""
+    import math
+
+    w = np.array(w0, dtype=np.float64)
+    m = np.zeros_like(w)
+    v = np.zeros_like(w)
+    out = []
+    for s, g in enumerate(np.asarray(grads, dtype=np.float64), start=1):
+        sg = (g / 1.0) * impedance * inv_record_steps
+        m = beta1 * m + (1.0 - beta1) * sg
+        v = beta2 * v + (1.0 - beta2) * sg * sg
+        b1 = math.pow(beta1, float(s))
+        b2 = math.pow(beta2, float(s))
+        mh = m / (1.0 - b1)
+        vh = v / (1.0 - b2)
+        w = w - lr * mh / (np.sqrt(vh) + eps)
+        out.append(w.copy())
+    return np.array(out), m, v
+
+
+def adam_ref(w0, grads, lr, inv_record_steps, beta1=0.9, beta2=0.999, eps=1e-8, impedance=1.0):
+    """The reference's own AdamOptimizer (CPU mode) through the harness."""
+    import tempfile
+
+    w0 = np.asarray(w0, dtype=np.float64)
+    grads = np.asarray(grads, dtype=np.float64)
+    n, steps = w0.shape[0], grads.shape[0]
+    with tempfile.TemporaryDirectory() as d:
+        fi, fo = os.path.join(d, "in.f64"), os.path.join(d, "out.f64")
+        np.concatenate([w0, grads.ravel()]).tofile(fi)
+        r = subprocess.run([REF_LIB, "--adam", str(n), str(steps), repr(lr), repr(inv_record_steps), repr(beta1),
+                            repr(beta2), repr(eps), repr(impedance), fi, fo], capture_output=True, text=True)
+        if r.returncode != 0:
+            raise RuntimeError(f"reference Adam failed ({r.returncode}): {r.stderr[-500:]}")
+        out = np.fromfile(fo, dtype=np.float64)
+    ws = out[: steps * n].reshape(steps, n)
+    return ws, out[steps * n: steps * n + n], out[steps * n + n:]
+
+
 def build() -> str:
     """Compile the oracle (make) and return the .so path."""
     subprocess.run(["make", "-s", "-C", _HERE], check=True)

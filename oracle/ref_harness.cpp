@@ -9,6 +9,11 @@
 // LearnRuntime::simulate_output_vs_into), and output_spikes into spike_dir.
 // Only permute type 0 (the reference's CPU default, src/main.cpp:149-152) is
 // used, so reference node i is the group's node i.
+//
+//   hxref_run --adam <n> <steps> <lr> <inv_record_steps> <beta1> <beta2> <eps> <impedance> <in.f64> <out.f64>
+// runs the reference's AdamOptimizer (src/optimizer/optimizer.cpp) on the CPU:
+// in.f64 holds n initial weights followed by steps x n gradients; out.f64
+// receives the weights after every step (steps x n) and the final m and v.
 #include <cstdio>
 #include <cstdlib>
 #include <memory>
@@ -17,11 +22,54 @@
 
 #include "coredat_to_innerdat.h"
 #include "read_coredat.h"
+#include "optimizer/optimizer.h"
 #include "simulate.h"
 
 extern int permute_type;
 
+static int run_adam(int argc, char** argv) {
+    if (argc != 12) return 2;
+    const int n = std::atoi(argv[2]), steps = std::atoi(argv[3]);
+    const double lr = std::atof(argv[4]), inv = std::atof(argv[5]);
+    OptimizerHyperParams hp;
+    hp.beta1 = std::atof(argv[6]);
+    hp.beta2 = std::atof(argv[7]);
+    hp.epsilon = std::atof(argv[8]);
+    const double imp = std::atof(argv[9]);
+    std::vector<double> in((size_t)n * (steps + 1));
+    FILE* f = std::fopen(argv[10], "rb");
+    if (!f || std::fread(in.data(), sizeof(double), in.size(), f) != in.size()) return 3;
+    std::fclose(f);
+    std::vector<double> w(in.begin(), in.begin() + n), g(n, 0.0);
+    AdamOptimizer opt(CPU);
+    opt.configure(hp);
+    for (int i = 0; i < n; i++) {
+        OptimizerParam prm;
+        prm.weight_cpu = {&w[i]};
+        prm.grad_cpu = {&g[i]};
+        prm.impedance = imp;
+        if (opt.add_param(prm) < 0) return 4;
+    }
+    std::vector<double> out;
+    for (int s = 0; s < steps; s++) {
+        for (int i = 0; i < n; i++) g[i] = in[(size_t)(s + 1) * n + i];
+        opt.step(lr, inv);
+        out.insert(out.end(), w.begin(), w.end());
+    }
+    long long sc = 0;
+    std::vector<double> m, v;
+    opt.export_state(sc, m, v);
+    out.insert(out.end(), m.begin(), m.end());
+    out.insert(out.end(), v.begin(), v.end());
+    f = std::fopen(argv[11], "wb");
+    if (!f) return 3;
+    std::fwrite(out.data(), sizeof(double), out.size(), f);
+    std::fclose(f);
+    return 0;
+}
+
 int main(int argc, char** argv) {
+    if (argc > 1 && std::string(argv[1]) == "--adam") return run_adam(argc, argv);
     if (argc != 9) {
         std::fprintf(stderr, "usage: %s dir permute_type dt nstep v_init probes.i32 trace.f64 spike_dir\n", argv[0]);
         return 2;

@@ -30,7 +30,22 @@ CASES = {
 }
 
 
+ADAM = dict(n=64, steps=25, lr=1e-3, inv_record_steps=0.25, beta1=0.9, beta2=0.999, eps=1e-8, impedance=2.0, seed=5)
+
+
+def adam_inputs():
+    rng = np.random.default_rng(ADAM["seed"])
+    w0 = rng.uniform(0.01, 0.2, ADAM["n"])
+    grads = rng.standard_normal((ADAM["steps"], ADAM["n"])) * 10.0
+    return w0, grads
+
+
 def main():
+    w0, grads = adam_inputs()
+    ws, m, v = O.adam_ref(w0, grads, ADAM["lr"], ADAM["inv_record_steps"], ADAM["beta1"], ADAM["beta2"], ADAM["eps"],
+                          ADAM["impedance"])
+    np.savez_compressed(os.path.join(HERE, "adam.npz"), w0=w0, grads=grads, weights=ws, m=m, v=v)
+    print("adam", ws.shape)
     for name, (make, nstep, probes) in CASES.items():
         g = make()
         p = np.asarray(probes if probes is not None else list(g.soma_nodes()) + [g.nnode - 1], dtype=np.int32)

@@ -18,7 +18,7 @@ from heliox_b200 import synth
 from oracle import oracle as O
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-GOLDEN = sorted(glob.glob(os.path.join(HERE, "golden", "*.npz")))
+GOLDEN = sorted(p for p in glob.glob(os.path.join(HERE, "golden", "*.npz")) if not p.endswith("adam.npz"))
 
 import importlib.util
 
@@ -78,3 +78,12 @@ def test_adjoint_vs_fd_of_reference_forward():
         fd = (-L(tab, field, j, x0 + 2 * h) + 8 * L(tab, field, j, x0 + h) - 8 * L(tab, field, j, x0 - h)
               + L(tab, field, j, x0 - 2 * h)) / (12 * h)
         assert abs(gr[key][j] - fd) <= 2e-6 * abs(fd), (key, gr[key][j], fd)
+
+
+def test_adam_port_bit_exact_vs_reference_golden():
+    d = np.load(os.path.join(HERE, "golden", "adam.npz"))
+    a = _mg.ADAM
+    ws, m, v = O.adam_port(d["w0"], d["grads"], a["lr"], a["inv_record_steps"], a["beta1"], a["beta2"], a["eps"],
+                           a["impedance"])
+    assert np.array_equal(ws, d["weights"])
+    assert np.array_equal(m, d["m"]) and np.array_equal(v, d["v"])
