@@ -10,12 +10,22 @@ Writes the files the reference loads with ``read_coredat``
 
 Mechanism data columns follow the offsets the reference reads
 (``var_in_coredata_idx`` of hh_templated.cu:51-65, pas_templated.cu:13-14,
-iclamp_templated.cu:25-27, capac.cpp:29, eion.cuh:81-86); the remaining
+iclamp_templated.cu:25-27, capac.cpp:29, eion.cuh:81-86, expsyn.cpp:36-72,
+exp2syn_temp.cuh:22-27, netstim.cpp:56-79, HalfGap.cu:43-47,
+gapjunction_lr.cu:47-53, neuron_to_neuron_syn_lr.cu:70-86); the remaining
 columns of NEURON's layouts are written as zeros.  Ion instances (na_ion, k_ion)
 sit on every hh node and carry the reversal potentials; their ``iontype``
 flags are 0 (fixed reversal potentials, eion.cuh:155-197).  Every cell gets a
-spike-source PreSyn at its root (gid = cell index, threshold 10 mV), which the
-loader requires for each real cell (read_coredat.cpp:911-915).
+spike-source PreSyn at its root (gid = cell index, threshold ``ps_thresh``),
+which the loader requires for each real cell (read_coredat.cpp:911-915);
+NetStim j gets PreSyn ``ncell + j`` (gid ``ncell + j``).  Point processes carry
+dparams (area node, point-process slot[, POINTER target node]); POINTERs of
+gapjunction_lr / neuron_to_neuron_syn_lr are voltages (empty pointer2type,
+mech_template.cuh:431-455).  One NetCon per ExpSyn / Exp2Syn instance, ExpSyn
+targets first, in instance order.  HalfGap's vgap is not in the files: the
+reference wires it through Simulate::add_gap_source/add_gap_target
+(simulate.cpp:995-1056); ``write_coredat`` writes the (instance, source node)
+pairs to ``halfgap.i32`` for a driver to replay.
 """
 from __future__ import annotations
 
@@ -38,12 +48,20 @@ MECH_TABLE: List[Tuple[int, str, int, int, int, int, int, float]] = [
     (6, "k_ion", 0, 0, 1, 5, 1, 1.0),
     (7, "hh", 0, 0, 0, 23, 0, 0.0),
     (8, "IClamp", 1, 0, 0, 4, 2, 0.0),
+    (9, "ExpSyn", 2, 0, 0, 8, 2, 0.0),
+    (10, "Exp2Syn", 3, 0, 0, 13, 2, 0.0),
+    (11, "NetStim", 4, 1, 0, 9, 2, 0.0),
+    (12, "HalfGap", 5, 0, 0, 5, 2, 0.0),
+    (13, "gapjunction_lr", 6, 0, 0, 7, 3, 0.0),
+    (14, "neuron_to_neuron_syn_lr", 7, 0, 0, 19, 3, 0.0),
 ]
+# a NetStim's PreSyn is written as output_vindex -(type + USER_MOD_NUM * index)
+# (read_coredat.cpp:930-940 with the loader's default user_mod_num 1000)
+USER_MOD_NUM = 1000
 TYPE = {m[1]: m[0] for m in MECH_TABLE}
 DSIZE = {m[1]: m[5] for m in MECH_TABLE}
 PDSIZE = {m[1]: m[6] for m in MECH_TABLE}
 
-SPIKE_THRESHOLD = 10.0
 
 
 class _Writer:
@@ -87,13 +105,21 @@ def write_coredat(g: CellGroup, path: str, file_id: int = 0) -> str:
 
     chk = [0]
     ncell = g.ncell
-    # <id>_1.dat: one PreSyn per cell (gid = cell index), no NetCons
+    nstim = g.netstim.n
+    npre = ncell + nstim
+    e1, e2 = g.expsyn, g.exp2syn
+    nc_src = np.concatenate([e1.ifields["src"], e2.ifields["src"]]).astype(np.int32)
+    nc_type = np.concatenate([np.full(e1.n, TYPE["ExpSyn"]), np.full(e2.n, TYPE["Exp2Syn"])]).astype(np.int32)
+    nc_index = np.concatenate([np.arange(e1.n), np.arange(e2.n)]).astype(np.int32)
+    nc_w = np.concatenate([e1.fields["weight"], e2.fields["weight"]])
+    nc_d = np.concatenate([e1.fields["delay"], e2.fields["delay"]])
+    # <id>_1.dat: PreSyns (cells, then NetStims; gid = index) and NetCon sources
     w = _Writer(os.path.join(path, f"{file_id}_1.dat"))
     w.line(VERSION)
-    w.line(ncell)  # n_presyn
-    w.line(0)  # n_netcon
-    w.array(chk, np.arange(ncell, dtype=np.int32))  # output_gid
-    w.array(chk, np.zeros(0, dtype=np.int32))  # netcon_srcgid
+    w.line(npre)  # n_presyn
+    w.line(nc_src.shape[0])  # n_netcon
+    w.array(chk, np.arange(npre, dtype=np.int32))  # output_gid
+    w.array(chk, nc_src)  # netcon_srcgid
     w.close()
 
     # mechanism instance tables in type order
@@ -119,52 +145,73 @@ def write_coredat(g: CellGroup, path: str, file_id: int = 0) -> str:
         d[:, 19] = hh.fields["ena"]
         d[:, 20] = hh.fields["ek"]
         mechs.append(("hh", hh.nodes, d, None))
-    npnt = 0
-    if ic.n:
-        d = np.zeros((ic.n, DSIZE["IClamp"]))
-        d[:, 0] = ic.fields["del"]
-        d[:, 1] = ic.fields["dur"]
-        d[:, 2] = ic.fields["amp"]
-        pd = np.zeros((ic.n, 2), dtype=np.int32)
-        pd[:, 0] = ic.nodes  # area of the node
-        pd[:, 1] = np.arange(ic.n) + npnt  # point-process slot in vdata
-        npnt += ic.n
-        mechs.append(("IClamp", ic.nodes, d, pd))
+    npnt = [0]
+
+    def point(name, tab, cols, pointer=None, nodes=None):
+        if not tab.n:
+            return
+        d = np.zeros((tab.n, DSIZE[name]))
+        for c, key in cols:
+            d[:, c] = tab.fields[key]
+        pd = np.zeros((tab.n, PDSIZE[name]), dtype=np.int32)
+        pd[:, 0] = tab.nodes if nodes is None else 0  # area of the node
+        pd[:, 1] = np.arange(tab.n) + npnt[0]  # point-process slot in vdata
+        if pointer is not None:
+            pd[:, 2] = pointer
+        npnt[0] += tab.n
+        mechs.append((name, tab.nodes if nodes is None else nodes, d, pd))
+
+    point("IClamp", ic, ((0, "del"), (1, "dur"), (2, "amp")))
+    point("ExpSyn", e1, ((0, "tau"), (1, "e")))
+    point("Exp2Syn", e2, ((0, "tau1"), (1, "tau2"), (2, "e")))
+    point("NetStim", g.netstim, ((0, "interval"), (1, "number"), (2, "start"), (3, "noise")),
+          nodes=np.zeros(0, dtype=np.int32))
+    point("HalfGap", g.halfgap, ((0, "g"),))
+    point("gapjunction_lr", g.gapjunction, ((0, "g"), (1, "w")), pointer=g.gapjunction.ifields["pre"])
+    point("neuron_to_neuron_syn_lr", g.graded, ((0, "w"), (1, "g"), (2, "delta"), (3, "k"), (4, "Vth"), (5, "erev"),
+                                                (6, "dvpre")), pointer=g.graded.ifields["pre"])
+    npnt = npnt[0]
+    counts = {name: (g.netstim.n if name == "NetStim" else int(nodes.shape[0])) for name, nodes, _, _ in mechs}
 
     # <id>_2.dat
     w = _Writer(os.path.join(path, f"{file_id}_2.dat"))
     w.line(VERSION)
     w.line(ncell)  # n_real_cell
-    w.line(ncell)  # n_outputgid (= n_presyn)
+    w.line(npre)  # n_outputgid (= n_presyn)
     w.line(ncell)  # n_real_output
     w.line(n)  # n_node
     w.line(0)  # n_diam
     w.line(len(mechs))
     for name, nodes, _, _ in mechs:
         w.line(TYPE[name])
-        w.line(int(nodes.shape[0]))
+        w.line(counts[name])
     w.line(0)  # nidata
     w.line(npnt)  # nvdata
-    w.line(0)  # n_weight
+    w.line(nc_src.shape[0])  # n_weight (pnt_receive_size 1 for ExpSyn and Exp2Syn)
     w.array(chk, g.parent.astype(np.int32))
     w.array(chk, g.a.astype(np.float64))
     w.array(chk, g.b.astype(np.float64))
     w.array(chk, g.area.astype(np.float64))
     w.array(chk, np.full(n, g.v_init, dtype=np.float64))
     for name, nodes, data, pdata in mechs:
-        w.array(chk, np.ascontiguousarray(nodes, dtype=np.int32))
+        if name != "NetStim":  # artificial cells have no nodeindices (read_coredat.cpp:748-757)
+            w.array(chk, np.ascontiguousarray(nodes, dtype=np.int32))
         w.array(chk, np.ascontiguousarray(data, dtype=np.float64).reshape(-1))
         if PDSIZE[name]:
             w.array(chk, np.ascontiguousarray(pdata, dtype=np.int32).reshape(-1))
             w.line(0)  # pointer2type size
             w.line(0)  # nmodlrandom size
-    w.array(chk, np.arange(ncell, dtype=np.int32))  # output_vindex: root node of each cell
-    w.array(chk, np.full(ncell, SPIKE_THRESHOLD))  # output_threshold
-    w.array(chk, np.zeros(0, dtype=np.int32))  # pnttype
-    w.array(chk, np.zeros(0, dtype=np.int32))  # pntindex
-    w.array(chk, np.zeros(0))  # weights
-    w.array(chk, np.zeros(0))  # delay
+    ovi = np.concatenate([np.arange(ncell), -(TYPE["NetStim"] + USER_MOD_NUM * np.arange(nstim))]).astype(np.int32)
+    w.array(chk, ovi)  # output_vindex: root node of each cell, encoded NetStim instances
+    w.array(chk, np.ascontiguousarray(g.ps_thresh, dtype=np.float64))  # output_threshold (real cells)
+    w.array(chk, nc_type)  # pnttype
+    w.array(chk, nc_index)  # pntindex
+    w.array(chk, np.ascontiguousarray(nc_w, dtype=np.float64))  # weights
+    w.array(chk, np.ascontiguousarray(nc_d, dtype=np.float64))  # delay
     w.line(0)  # BBCOREPOINTER count
     w.line(0)  # VecPlayContinuous count
     w.close()
+    if g.halfgap.n:
+        np.column_stack([np.arange(g.halfgap.n), g.halfgap.ifields["src"]]).astype(np.int32).tofile(
+            os.path.join(path, "halfgap.i32"))
     return path

@@ -13,9 +13,31 @@ NEURON sign convention consumed at ``src/simulate.cpp:544-555``), ``cm`` in
 uF/cm^2, conductances in S/cm^2, currents of point processes in nA, times in ms,
 voltages in mV.
 
-Mechanism order inside one step is the CoreNEURON type order that the reference
-keeps in ``mech_current_list`` (``src/io/coredat_to_innerdat.cpp:179-181``):
-capacitance, pas, hh, IClamp, ExpSyn, Exp2Syn, HalfGap, graded synapse.
+Mechanism order inside one step is the order of the CoreNEURON mechanism list
+that the reference keeps in ``mech_current_list``
+(``src/io/coredat_to_innerdat.cpp:179-181``); the exporter here writes it as
+capacitance, pas, hh, IClamp, ExpSyn, Exp2Syn, NetStim, HalfGap,
+gapjunction_lr, neuron_to_neuron_syn_lr.
+
+Network parts (all optional, empty by default):
+
+* ``expsyn`` / ``exp2syn``: event-driven synapses (fields tau / tau1, tau2, e),
+  each instance the target of exactly one NetCon: ``ifields['src']`` is the
+  spike source (0..ncell-1: the PreSyn of that cell; ncell+j: NetStim j),
+  ``fields['delay']`` (ms) and ``fields['weight']`` (uS) -- the per-instance
+  ``spk_vec_idx``/``delay``/``weights`` the reference fills in
+  ``initSynapse`` (coredat_to_innerdat.cpp:348-376);
+* ``ps_thresh``: spike threshold (mV) of each cell's PreSyn, detected at the
+  cell's root node (``PreSyn::threshold_detect_cpu``, presyn.cpp:133-177);
+* ``netstim``: artificial spike sources (fields interval, number, start,
+  noise; netstim.cpp), ``netstim_rng`` selects the initial random stream
+  (0: the reference's CPU mode, 1: its GPU mode);
+* ``halfgap``: HalfGap point processes (field g, ``ifields['src']`` the node
+  whose voltage is copied into vgap; HalfGap.cu, simulate.cpp:953-966);
+* ``gapjunction``: gapjunction_lr (fields g, w, ``ifields['pre']``,
+  gapjunction_lr.cu:58-65);
+* ``graded``: neuron_to_neuron_syn_lr (fields w, g, delta, k, Vth, erev,
+  dvpre, ``ifields['pre']``, neuron_to_neuron_syn_lr.cu:97-145).
 """
 from __future__ import annotations
 
@@ -32,6 +54,13 @@ I32 = np.int32
 HH_PARAMS = ("gnabar", "gkbar", "gl", "el")
 PAS_PARAMS = ("g", "e")
 ICLAMP_PARAMS = ("del", "dur", "amp")
+EXPSYN_FIELDS = ("tau", "e", "delay", "weight")
+EXP2SYN_FIELDS = ("tau1", "tau2", "e", "delay", "weight")
+NETSTIM_FIELDS = ("interval", "number", "start", "noise")
+HALFGAP_FIELDS = ("g",)
+GAPJ_FIELDS = ("g", "w")
+GRADED_FIELDS = ("w", "g", "delta", "k", "Vth", "erev", "dvpre")
+SPIKE_THRESHOLD = 10.0
 
 
 def _f64(x) -> np.ndarray:
@@ -44,17 +73,23 @@ def _i32(x) -> np.ndarray:
 
 @dataclass
 class MechTable:
-    """Instances of one mechanism: ``nodes`` (sorted, int32) + per-instance fields."""
+    """Instances of one mechanism: ``nodes`` (sorted, int32) + per-instance fields.
+
+    ``fields`` are float64 per-instance values; ``ifields`` are int32
+    per-instance values (a partner node, a spike source).
+    """
 
     nodes: np.ndarray
     fields: Dict[str, np.ndarray] = field(default_factory=dict)
+    ifields: Dict[str, np.ndarray] = field(default_factory=dict)
 
     @property
     def n(self) -> int:
         return int(self.nodes.shape[0])
 
     def copy(self) -> "MechTable":
-        return MechTable(self.nodes.copy(), {k: v.copy() for k, v in self.fields.items()})
+        return MechTable(self.nodes.copy(), {k: v.copy() for k, v in self.fields.items()},
+                         {k: v.copy() for k, v in self.ifields.items()})
 
 
 @dataclass
@@ -75,6 +110,41 @@ class CellGroup:
     v_init: float = -65.0
     name: str = "group"
     meta: Dict[str, object] = field(default_factory=dict)
+    expsyn: Optional[MechTable] = None
+    exp2syn: Optional[MechTable] = None
+    netstim: Optional[MechTable] = None
+    halfgap: Optional[MechTable] = None
+    gapjunction: Optional[MechTable] = None
+    graded: Optional[MechTable] = None
+    ps_thresh: Optional[np.ndarray] = None
+    netstim_rng: int = 0
+
+    def __post_init__(self):
+        if self.expsyn is None:
+            self.expsyn = empty_table(EXPSYN_FIELDS, ("src",))
+        if self.exp2syn is None:
+            self.exp2syn = empty_table(EXP2SYN_FIELDS, ("src",))
+        if self.netstim is None:
+            self.netstim = empty_table(NETSTIM_FIELDS)
+        if self.halfgap is None:
+            self.halfgap = empty_table(HALFGAP_FIELDS, ("src",))
+        if self.gapjunction is None:
+            self.gapjunction = empty_table(GAPJ_FIELDS, ("pre",))
+        if self.graded is None:
+            self.graded = empty_table(GRADED_FIELDS, ("pre",))
+        if self.ps_thresh is None:
+            self.ps_thresh = np.full(self.ncell, SPIKE_THRESHOLD)
+
+    @property
+    def has_network(self) -> bool:
+        """True if any event, gap or graded coupling is present."""
+        return bool(self.expsyn.n or self.exp2syn.n or self.netstim.n or self.halfgap.n or self.gapjunction.n
+                    or self.graded.n)
+
+    @property
+    def coupled(self) -> bool:
+        """True if voltages of other nodes enter a step's currents or states (gaps, graded synapses)."""
+        return bool(self.halfgap.n or self.gapjunction.n or self.graded.n)
 
     # ------------------------------------------------------------------ basics
     @property
@@ -119,6 +189,39 @@ class CellGroup:
             for k, v in tab.fields.items():
                 if v.shape != (tab.n,) or v.dtype != F64:
                     raise ValueError(f"{nm}.{k} must be float64[{tab.n}]")
+        nsrc = self.ncell + self.netstim.n
+        for tab, nm, fl in ((self.expsyn, "ExpSyn", EXPSYN_FIELDS), (self.exp2syn, "Exp2Syn", EXP2SYN_FIELDS),
+                            (self.halfgap, "HalfGap", HALFGAP_FIELDS), (self.gapjunction, "gapjunction_lr",
+                                                                        GAPJ_FIELDS),
+                            (self.graded, "neuron_to_neuron_syn_lr", GRADED_FIELDS)):
+            if tab.n and (np.any(tab.nodes < 0) or np.any(tab.nodes >= n)):
+                raise ValueError(f"{nm} node index out of range")
+            if tab.n > 1 and np.any(np.diff(tab.nodes) < 0):
+                raise ValueError(f"{nm} nodes must be sorted")
+            for k in fl:
+                v = tab.fields.get(k)
+                if v is None or v.shape != (tab.n,) or v.dtype != F64:
+                    raise ValueError(f"{nm}.{k} must be float64[{tab.n}]")
+            for k, v in tab.ifields.items():
+                if v.shape != (tab.n,) or v.dtype != I32:
+                    raise ValueError(f"{nm}.{k} must be int32[{tab.n}]")
+        for tab, nm in ((self.expsyn, "ExpSyn"), (self.exp2syn, "Exp2Syn")):
+            src = tab.ifields.get("src")
+            if src is None or (tab.n and (np.any(src < 0) or np.any(src >= nsrc))):
+                raise ValueError(f"{nm}.src must index a cell PreSyn (0..ncell-1) or a NetStim (ncell..)")
+            if tab.n and np.any(tab.fields["delay"] < self.dt):
+                raise ValueError(f"{nm}: NetCon delays must be at least dt (one step)")
+        for tab, nm, key in ((self.halfgap, "HalfGap", "src"), (self.gapjunction, "gapjunction_lr", "pre"),
+                             (self.graded, "neuron_to_neuron_syn_lr", "pre")):
+            pv = tab.ifields.get(key)
+            if pv is None or (tab.n and (np.any(pv < 0) or np.any(pv >= n))):
+                raise ValueError(f"{nm}.{key} must be a node index")
+        if self.exp2syn.n and np.any(self.exp2syn.fields["tau2"] <= 0):
+            raise ValueError("Exp2Syn.tau2 must be positive")
+        if self.expsyn.n and np.any(self.expsyn.fields["tau"] <= 0):
+            raise ValueError("ExpSyn.tau must be positive")
+        if self.ps_thresh.shape != (self.ncell,) or self.ps_thresh.dtype != F64:
+            raise ValueError(f"ps_thresh must be float64[{self.ncell}]")
 
     def copy(self) -> "CellGroup":
         return CellGroup(
@@ -136,12 +239,22 @@ class CellGroup:
             v_init=self.v_init,
             name=self.name,
             meta=dict(self.meta),
+            expsyn=self.expsyn.copy(),
+            exp2syn=self.exp2syn.copy(),
+            netstim=self.netstim.copy(),
+            halfgap=self.halfgap.copy(),
+            gapjunction=self.gapjunction.copy(),
+            graded=self.graded.copy(),
+            ps_thresh=self.ps_thresh.copy(),
+            netstim_rng=self.netstim_rng,
         )
 
     # ------------------------------------------------------------ parameters
     def param_view(self, mech: str, var: str) -> np.ndarray:
         """The live array of one learnable/settable parameter."""
-        tab = {"hh": self.hh, "pas": self.pas, "IClamp": self.iclamp}.get(mech)
+        tab = {"hh": self.hh, "pas": self.pas, "IClamp": self.iclamp, "ExpSyn": self.expsyn,
+               "Exp2Syn": self.exp2syn, "NetStim": self.netstim, "HalfGap": self.halfgap,
+               "gapjunction_lr": self.gapjunction, "neuron_to_neuron_syn_lr": self.graded}.get(mech)
         if tab is None:
             if mech == "capacitance" and var == "cm":
                 return self.cm
@@ -152,8 +265,8 @@ class CellGroup:
         return tab.fields[key]
 
 
-def empty_table(names) -> MechTable:
-    return MechTable(_i32([]), {k: _f64([]) for k in names})
+def empty_table(names, inames=()) -> MechTable:
+    return MechTable(_i32([]), {k: _f64([]) for k in names}, {k: _i32([]) for k in inames})
 
 
 def concat_groups(groups, name: str = "group") -> CellGroup:

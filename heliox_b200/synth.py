@@ -235,3 +235,176 @@ def perturb_conductances(g: CellGroup, sigma: float = 0.2, seed: int = 99) -> Ce
         t.hh.fields[k] = _f64(t.hh.fields[k] * np.exp(sigma * rng.standard_normal(t.hh.n)))
     t.pas.fields["g"] = _f64(t.pas.fields["g"] * np.exp(sigma * rng.standard_normal(t.pas.n)))
     return t
+
+
+# ---------------------------------------------------------------- networks
+def _table(nodes, fields, ifields=None) -> MechTable:
+    """Instance table sorted by node (stable), the layout the exporter writes."""
+    nodes = np.asarray(nodes, dtype=np.int64)
+    o = np.argsort(nodes, kind="stable")
+    return MechTable(_i32(nodes[o]), {k: _f64(np.asarray(v, dtype=np.float64)[o]) for k, v in fields.items()},
+                     {k: _i32(np.asarray(v)[o]) for k, v in (ifields or {}).items()})
+
+
+def _cell_nodes(g: CellGroup) -> List[np.ndarray]:
+    cell = g.cell_of_node()
+    order = np.argsort(cell, kind="stable")
+    bounds = np.searchsorted(cell[order], np.arange(g.ncell + 1))
+    return [order[bounds[c]:bounds[c + 1]] for c in range(g.ncell)]
+
+
+def spiking_network(ncell: int = 8, seed: int = 11, nmin: int = 40, nmax: int = 120, syn_per_cell: int = 6,
+                    nstim: int = 4, exp_frac: float = 0.3, weight: Tuple[float, float] = (0.005, 0.03),
+                    delay: Tuple[float, float] = (1.0, 5.0), drive_frac: float = 0.5,
+                    stim_interval: float = 8.0, stim_number: float = 20.0, stim_noise: float = 0.5) -> CellGroup:
+    """A small event-driven network of random-tree cells (test scale).
+
+    Every cell receives ``syn_per_cell`` synapses at uniformly drawn nodes of
+    its own tree (a fraction ``exp_frac`` ExpSyn with tau 2 ms, the rest
+    Exp2Syn with tau1 0.5, tau2 5 ms), each driven by one NetCon from a random
+    other cell (80 % excitatory, e = 0 mV; 20 % inhibitory, e = -80 mV) with
+    delay U[delay] and weight U[weight] uS.  ``nstim`` NetStims (interval,
+    number, start 1 ms, noise) each drive one extra Exp2Syn at the soma of
+    cell ``i % ncell``.  Only a fraction ``drive_frac`` of the cells keep
+    their somatic IClamp.
+    """
+    rng = np.random.default_rng(seed)
+    cells = [random_tree_cell(seed * 1000 + c, nmin=nmin, nmax=nmax) for c in range(ncell)]
+    g = concat_groups(cells, name=f"net{ncell}")
+    amp = g.iclamp.fields["amp"].copy()
+    amp[rng.random(amp.shape[0]) >= drive_frac] = 0.0
+    g.iclamp.fields["amp"] = _f64(amp)
+    per_cell = _cell_nodes(g)
+    e1 = {"nodes": [], "tau": [], "e": [], "delay": [], "weight": [], "src": []}
+    e2 = {"nodes": [], "tau1": [], "tau2": [], "e": [], "delay": [], "weight": [], "src": []}
+    for c in range(ncell):
+        for _ in range(syn_per_cell):
+            node = int(rng.choice(per_cell[c]))
+            src = int(rng.integers(ncell - 1))
+            src = src + 1 if src >= c else src
+            e = 0.0 if rng.random() < 0.8 else -80.0
+            d = float(rng.uniform(*delay))
+            w = float(rng.uniform(*weight))
+            if rng.random() < exp_frac:
+                for k, v in zip(("nodes", "tau", "e", "delay", "weight", "src"), (node, 2.0, e, d, w, src)):
+                    e1[k].append(v)
+            else:
+                for k, v in zip(("nodes", "tau1", "tau2", "e", "delay", "weight", "src"),
+                                (node, 0.5, 5.0, e, d, w, src)):
+                    e2[k].append(v)
+    for i in range(nstim):
+        for k, v in zip(("nodes", "tau1", "tau2", "e", "delay", "weight", "src"),
+                        (i % ncell, 0.5, 5.0, 0.0, float(rng.uniform(*delay)), 2 * weight[1], ncell + i)):
+            e2[k].append(v)
+    g.expsyn = _table(e1["nodes"], {k: e1[k] for k in ("tau", "e", "delay", "weight")}, {"src": e1["src"]})
+    g.exp2syn = _table(e2["nodes"], {k: e2[k] for k in ("tau1", "tau2", "e", "delay", "weight")}, {"src": e2["src"]})
+    g.netstim = MechTable(_i32(np.zeros(nstim)), {
+        "interval": _f64(np.full(nstim, stim_interval)), "number": _f64(np.full(nstim, stim_number)),
+        "start": _f64(np.full(nstim, 1.0)), "noise": _f64(np.full(nstim, stim_noise))})
+    g.validate()
+    return g
+
+
+def network_config4(ncell: int = 10000, seed: int = 4, syn_per_cell: int = 100, nmin: int = 400, nmax: int = 600,
+                    rate_hz: float = 5.0) -> CellGroup:
+    """Config 4: ``ncell`` random-tree cells, ``syn_per_cell`` Exp2Syn each.
+
+    80/20 excitatory/inhibitory sources (e = 0 / -80 mV), tau1 0.5, tau2 5 ms,
+    weight exp(N(-7, 1)) uS, random presynaptic cell, delay U[1, 5] ms; one
+    NetStim per cell (``rate_hz``, noise 1, start 0, unlimited number) drives
+    one more Exp2Syn at the soma.  Seeded; the reference quotes no data set.
+    """
+    rng = np.random.default_rng(seed)
+    cells = [random_tree_cell(seed * 100000 + c, nmin=nmin, nmax=nmax) for c in range(ncell)]
+    g = concat_groups(cells, name=f"net{ncell}")
+    cell = g.cell_of_node()
+    order = np.argsort(cell, kind="stable")
+    bounds = np.searchsorted(cell[order], np.arange(ncell + 1))
+    nsyn = ncell * syn_per_cell
+    post = np.repeat(np.arange(ncell), syn_per_cell)
+    pick = bounds[post] + (rng.random(nsyn) * (bounds[post + 1] - bounds[post])).astype(np.int64)
+    nodes = order[pick]
+    src = rng.integers(0, ncell - 1, nsyn)
+    src = np.where(src >= post, src + 1, src)
+    exc = rng.random(nsyn) < 0.8
+    e = np.where(exc, 0.0, -80.0)
+    d = rng.uniform(1.0, 5.0, nsyn)
+    w = np.exp(rng.normal(-7.0, 1.0, nsyn))
+    nodes = np.concatenate([nodes, np.arange(ncell)])
+    src = np.concatenate([src, ncell + np.arange(ncell)])
+    e = np.concatenate([e, np.zeros(ncell)])
+    d = np.concatenate([d, rng.uniform(1.0, 5.0, ncell)])
+    w = np.concatenate([w, np.full(ncell, 0.01)])
+    n = nodes.shape[0]
+    g.exp2syn = _table(nodes, {"tau1": np.full(n, 0.5), "tau2": np.full(n, 5.0), "e": e, "delay": d, "weight": w},
+                       {"src": src})
+    g.netstim = MechTable(_i32(np.zeros(ncell)), {
+        "interval": _f64(np.full(ncell, 1000.0 / rate_hz)), "number": _f64(np.full(ncell, 1e9)),
+        "start": _f64(np.zeros(ncell)), "noise": _f64(np.ones(ncell))})
+    g.validate()
+    return g
+
+
+def coupled_network(ncell: int = 6, seed: int = 5, nmin: int = 50, nmax: int = 150, ngap: int = 6,
+                    ngapj: int = 3, ngraded: int = 10, drive_frac: float = 0.4,
+                    gap_g: Tuple[float, float] = (1e-4, 1e-3), graded_w: Tuple[float, float] = (2e-4, 2e-3)) -> CellGroup:
+    """Config 5 style network: cells coupled by gap junctions and graded synapses.
+
+    ``ngap`` HalfGap pairs (two instances per pair at random nodes of two
+    different cells, each copying the other's voltage, g U[gap_g] uS),
+    ``ngapj`` gapjunction_lr pairs (w 1, g U[gap_g]), ``ngraded``
+    neuron_to_neuron_syn_lr synapses from a random cell's soma onto a random
+    node of another cell (w = +-U[graded_w], 80 % positive; delta 5 mV,
+    Vth -20 mV, the MOD defaults otherwise).  A fraction ``drive_frac`` of the
+    cells keep their somatic IClamp.
+    """
+    rng = np.random.default_rng(seed)
+    cells = [random_tree_cell(seed * 1000 + c, nmin=nmin, nmax=nmax) for c in range(ncell)]
+    g = concat_groups(cells, name=f"coupled{ncell}")
+    amp = g.iclamp.fields["amp"].copy()
+    amp[rng.random(amp.shape[0]) >= drive_frac] = 0.0
+    g.iclamp.fields["amp"] = _f64(amp)
+    per_cell = _cell_nodes(g)
+
+    def two_cells():
+        a = int(rng.integers(ncell))
+        b = int(rng.integers(ncell - 1))
+        return a, (b + 1 if b >= a else b)
+
+    hn, hs, hg = [], [], []
+    for _ in range(ngap):
+        a, b = two_cells()
+        na, nb = int(rng.choice(per_cell[a])), int(rng.choice(per_cell[b]))
+        gg = float(rng.uniform(*gap_g))
+        hn += [na, nb]
+        hs += [nb, na]
+        hg += [gg, gg]
+    jn, jp, jg = [], [], []
+    for _ in range(ngapj):
+        a, b = two_cells()
+        na, nb = int(rng.choice(per_cell[a])), int(rng.choice(per_cell[b]))
+        gg = float(rng.uniform(*gap_g))
+        jn += [na, nb]
+        jp += [nb, na]
+        jg += [gg, gg]
+    rn, rp, rw = [], [], []
+    for _ in range(ngraded):
+        a, b = two_cells()
+        rn.append(int(rng.choice(per_cell[b])))
+        rp.append(a)
+        w = float(rng.uniform(*graded_w))
+        rw.append(w if rng.random() < 0.8 else -w)
+    g.halfgap = _table(hn, {"g": hg}, {"src": hs})
+    g.gapjunction = _table(jn, {"g": jg, "w": np.ones(len(jn))}, {"pre": jp})
+    ng = len(rn)
+    g.graded = _table(rn, {"w": rw, "g": np.full(ng, 4.9), "delta": np.full(ng, 5.0), "k": np.full(ng, 0.5),
+                           "Vth": np.full(ng, -20.0), "erev": np.full(ng, 30.0), "dvpre": np.full(ng, 1e-3)},
+                      {"pre": rp})
+    g.validate()
+    return g
+
+
+def worm_config5(ncell: int = 302, seed: int = 5) -> CellGroup:
+    """Config 5: 302 cells of U[50,150] compartments, 900 gap pairs, 2000 graded synapses."""
+    return coupled_network(ncell=ncell, seed=seed, nmin=50, nmax=150, ngap=900, ngapj=0, ngraded=2000,
+                           drive_frac=0.3)

@@ -19,6 +19,38 @@
 extern "C" {
 #endif
 
+/* Network parts (optional; hxo_group.net may be NULL).  Synapse instance
+ * tables are node-sorted like the reference's nodeindices; every ExpSyn /
+ * Exp2Syn instance is the target of one NetCon (src, delay, weight).  Sources
+ * 0..ncell-1 are the cells' PreSyns (threshold detection at the cell's root
+ * node), sources ncell.. are the NetStims in instance order. */
+typedef struct hxo_net {
+    int nexp;
+    const int *exp_node, *exp_src;
+    const double *exp_tau, *exp_e, *exp_delay, *exp_w;
+    int nexp2;
+    const int *exp2_node, *exp2_src;
+    const double *exp2_tau1, *exp2_tau2, *exp2_e, *exp2_delay, *exp2_w;
+    const double* ps_thresh; /* ncell */
+    int nstim;
+    const double *ns_interval, *ns_number, *ns_start, *ns_noise;
+    int rng_mode; /* 0: reference CPU mode (zero-initialised Random123 state), 1: GPU mode (sequence 0) */
+    int nhg;
+    const int *hg_node, *hg_src;
+    const double* hg_g;
+    int ngj;
+    const int *gj_node, *gj_pre;
+    const double *gj_g, *gj_w;
+    int ngr;
+    const int *gr_node, *gr_pre;
+    const double *gr_w, *gr_g, *gr_delta, *gr_k, *gr_vth, *gr_erev;
+    /* outputs of the forward: spikes of the cells' PreSyns (gid = cell, time) */
+    int spike_cap;
+    int* spike_gid;
+    double* spike_t;
+    int nspike; /* total detected (may exceed spike_cap) */
+} hxo_net;
+
 typedef struct hxo_group {
     int ncell, nnode;
     const int* parent;            /* -1 for the ncell roots, parent[i] < i otherwise */
@@ -33,6 +65,7 @@ typedef struct hxo_group {
     int nic;
     const int* ic_node;
     const double *ic_del, *ic_dur, *ic_amp;
+    hxo_net* net;
 } hxo_group;
 
 /* Gradient outputs; any pointer may be NULL.  Each array is per instance of its
@@ -42,6 +75,8 @@ typedef struct hxo_grads {
     double *pas_g, *pas_e;
     double *cm;
     double *ic_amp;
+    double *exp_w, *exp_e, *exp2_w, *exp2_e; /* per ExpSyn / Exp2Syn instance */
+    double *hg_g, *gj_g, *gj_w, *gr_w;       /* per HalfGap / gapjunction_lr / graded instance */
 } hxo_grads;
 
 /* Forward: finitialize(v_init) then nstep fadvance steps.

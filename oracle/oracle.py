@@ -20,6 +20,23 @@ _dp = C.POINTER(C.c_double)
 _ip = C.POINTER(C.c_int)
 
 
+class _Net(C.Structure):
+    _fields_ = [
+        ("nexp", C.c_int), ("exp_node", _ip), ("exp_src", _ip),
+        ("exp_tau", _dp), ("exp_e", _dp), ("exp_delay", _dp), ("exp_w", _dp),
+        ("nexp2", C.c_int), ("exp2_node", _ip), ("exp2_src", _ip),
+        ("exp2_tau1", _dp), ("exp2_tau2", _dp), ("exp2_e", _dp), ("exp2_delay", _dp), ("exp2_w", _dp),
+        ("ps_thresh", _dp),
+        ("nstim", C.c_int), ("ns_interval", _dp), ("ns_number", _dp), ("ns_start", _dp), ("ns_noise", _dp),
+        ("rng_mode", C.c_int),
+        ("nhg", C.c_int), ("hg_node", _ip), ("hg_src", _ip), ("hg_g", _dp),
+        ("ngj", C.c_int), ("gj_node", _ip), ("gj_pre", _ip), ("gj_g", _dp), ("gj_w", _dp),
+        ("ngr", C.c_int), ("gr_node", _ip), ("gr_pre", _ip), ("gr_w", _dp), ("gr_g", _dp), ("gr_delta", _dp),
+        ("gr_k", _dp), ("gr_vth", _dp), ("gr_erev", _dp),
+        ("spike_cap", C.c_int), ("spike_gid", _ip), ("spike_t", _dp), ("nspike", C.c_int),
+    ]
+
+
 class _Group(C.Structure):
     _fields_ = [
         ("ncell", C.c_int),
@@ -48,6 +65,7 @@ class _Group(C.Structure):
         ("ic_del", _dp),
         ("ic_dur", _dp),
         ("ic_amp", _dp),
+        ("net", C.POINTER(_Net)),
     ]
 
 
@@ -61,6 +79,8 @@ class _Grads(C.Structure):
         ("pas_e", _dp),
         ("cm", _dp),
         ("ic_amp", _dp),
+        ("exp_w", _dp), ("exp_e", _dp), ("exp2_w", _dp), ("exp2_e", _dp),
+        ("hg_g", _dp), ("gj_g", _dp), ("gj_w", _dp), ("gr_w", _dp),
     ]
 
 
@@ -220,7 +240,44 @@ class _Bound:
         s.nic = c.n
         s.ic_node = I(c.nodes)
         s.ic_del, s.ic_dur, s.ic_amp = D(c.fields["del"]), D(c.fields["dur"]), D(c.fields["amp"])
+        self.net = None
+        if g.has_network:
+            n = _Net()
+            e1, e2 = g.expsyn, g.exp2syn
+            n.nexp, n.exp_node, n.exp_src = e1.n, I(e1.nodes), I(e1.ifields["src"])
+            n.exp_tau, n.exp_e, n.exp_delay, n.exp_w = (D(e1.fields[k]) for k in ("tau", "e", "delay", "weight"))
+            n.nexp2, n.exp2_node, n.exp2_src = e2.n, I(e2.nodes), I(e2.ifields["src"])
+            n.exp2_tau1, n.exp2_tau2, n.exp2_e, n.exp2_delay, n.exp2_w = (
+                D(e2.fields[k]) for k in ("tau1", "tau2", "e", "delay", "weight"))
+            n.ps_thresh = D(g.ps_thresh)
+            ns = g.netstim
+            n.nstim = ns.n
+            n.ns_interval, n.ns_number, n.ns_start, n.ns_noise = (
+                D(ns.fields[k]) for k in ("interval", "number", "start", "noise"))
+            n.rng_mode = int(g.netstim_rng)
+            hg = g.halfgap
+            n.nhg, n.hg_node, n.hg_src, n.hg_g = hg.n, I(hg.nodes), I(hg.ifields["src"]), D(hg.fields["g"])
+            gj = g.gapjunction
+            n.ngj, n.gj_node, n.gj_pre = gj.n, I(gj.nodes), I(gj.ifields["pre"])
+            n.gj_g, n.gj_w = D(gj.fields["g"]), D(gj.fields["w"])
+            gr = g.graded
+            n.ngr, n.gr_node, n.gr_pre = gr.n, I(gr.nodes), I(gr.ifields["pre"])
+            n.gr_w, n.gr_g, n.gr_delta, n.gr_k, n.gr_vth, n.gr_erev = (
+                D(gr.fields[k]) for k in ("w", "g", "delta", "k", "Vth", "erev"))
+            cap = 1 << 16
+            self.spk_gid = np.zeros(cap, dtype=np.int32)
+            self.spk_t = np.zeros(cap)
+            n.spike_cap, n.spike_gid, n.spike_t, n.nspike = cap, _i(self.spk_gid), _d(self.spk_t), 0
+            self.net = n
+            s.net = C.pointer(n)
         self.s = s
+
+    def spikes(self):
+        """Detected PreSyn spikes as a list of (t, gid) in detection order."""
+        if self.net is None:
+            return []
+        k = min(self.net.nspike, self.net.spike_cap)
+        return [(float(self.spk_t[i]), int(self.spk_gid[i])) for i in range(k)]
 
 
 def forward(g, nstep: int, probe: Optional[Sequence[int]] = None, v_init: Optional[float] = None):
@@ -236,10 +293,12 @@ def forward(g, nstep: int, probe: Optional[Sequence[int]] = None, v_init: Option
                        _i(probe), _d(trace), _d(vf), _d(mf), _d(hf), _d(nf))
     if rc != 0:
         raise RuntimeError("oracle forward failed")
-    return trace, {"v": vf, "m": mf[: g.hh.n], "h": hf[: g.hh.n], "n": nf[: g.hh.n]}
+    return trace, {"v": vf, "m": mf[: g.hh.n], "h": hf[: g.hh.n], "n": nf[: g.hh.n], "spikes": b.spikes()}
 
 
 GRAD_KEYS = ("hh.gnabar", "hh.gkbar", "hh.gl", "hh.el", "pas.g", "pas.e", "cm", "IClamp.amp")
+NET_GRAD_KEYS = ("ExpSyn.weight", "ExpSyn.e", "Exp2Syn.weight", "Exp2Syn.e", "HalfGap.g", "gapjunction_lr.g",
+                 "gapjunction_lr.w", "neuron_to_neuron_syn_lr.w")
 
 
 def adjoint(g, nstep: int, dLdv: np.ndarray, probe: Optional[Sequence[int]] = None, v_init: Optional[float] = None):
@@ -264,8 +323,17 @@ def adjoint(g, nstep: int, dLdv: np.ndarray, probe: Optional[Sequence[int]] = No
     gs = _Grads()
     gs.hh_gnabar, gs.hh_gkbar, gs.hh_gl, gs.hh_el = (_d(out[k]) for k in GRAD_KEYS[:4])
     gs.pas_g, gs.pas_e, gs.cm, gs.ic_amp = (_d(out[k]) for k in GRAD_KEYS[4:])
+    if g.has_network:
+        sizes = (g.expsyn.n, g.expsyn.n, g.exp2syn.n, g.exp2syn.n, g.halfgap.n, g.gapjunction.n, g.gapjunction.n,
+                 g.graded.n)
+        for k, nsz in zip(NET_GRAD_KEYS, sizes):
+            out[k] = np.zeros(nsz)
+        gs.exp_w, gs.exp_e, gs.exp2_w, gs.exp2_e, gs.hg_g, gs.gj_g, gs.gj_w, gs.gr_w = (
+            _d(out[k]) for k in NET_GRAD_KEYS)
     rc = L.hxo_adjoint(C.byref(b.s), float(g.v_init if v_init is None else v_init), int(nstep), int(probe.shape[0]),
                        _i(probe), _d(dLdv), _d(trace), C.byref(gs))
     if rc != 0:
         raise RuntimeError("oracle adjoint failed")
+    if g.has_network:
+        out["spikes"] = b.spikes()
     return trace, out

@@ -1,7 +1,9 @@
 // ref_harness.cpp -- TEST INFRASTRUCTURE ONLY.
 //
 // Runs the reference's own CPU integrator on a CoreNEURON-format model
-// directory and writes the voltage trace at the requested nodes:
+// directory (plus halfgap.i32, HalfGap (instance, source node) pairs replayed
+// through Simulate::add_gap_source/add_gap_target) and writes the voltage
+// trace at the requested nodes:
 //   hxref_run <dir> <permute_type> <dt> <nstep> <v_init> <probes.i32> <trace.f64> <spike_dir>
 // It follows the reference's own driver (src/main.cpp:180-233): read_coredat,
 // Simulate(CPU), data_format_trans, finitialize, then fadvance per step (the
@@ -102,6 +104,22 @@ int main(int argc, char** argv) {
     data_format_trans(sim->neuron_group_list, arr, ngroup, CPU, sim->dt);
     for (int i = 0; i < ngroup; i++) delete arr[i];
     sim->permute_type = ptype;
+    // HalfGap: vgap of instance i follows the voltage of a source node, wired
+    // through the reference's gap API (pairs written by the exporter)
+    {
+        FILE* f = std::fopen((dir + "/halfgap.i32").c_str(), "rb");
+        if (f) {
+            int pr[2];
+            while (std::fread(pr, sizeof(int), 2, f) == 2) {
+                const int sid = sim->add_gap_source("global", "v", pr[1]);
+                if (sid < 0 || sim->add_gap_target(sid, "HalfGap", "vgap", pr[0]) != 0) {
+                    std::fprintf(stderr, "gap wiring failed for instance %d\n", pr[0]);
+                    return 4;
+                }
+            }
+            std::fclose(f);
+        }
+    }
     std::vector<VarDescriptor> monitors;
     sim->init_monitor_data_sets(monitors);
     sim->finitialize(v_init);

@@ -8,7 +8,8 @@ oracle/ref_build.sh); run from the repository root:
 Each case exports a seeded synthetic group in CoreNEURON format
 (heliox_b200.coredat), runs the reference (read_coredat -> data_format_trans ->
 Simulate(CPU) finitialize + fadvance) and stores the voltage trace at the
-probes together with the spike list the reference writes (spk.dat).
+probes together with the spike list the reference writes (spk.dat: time with
+8 significant digits, gid).
 """
 import os
 import sys
@@ -27,6 +28,11 @@ CASES = {
     "ball_and_stick_teacher": (lambda: synth.ball_and_stick(gnabar_scale=1.1), 4000, [0]),
     "trees3": (lambda: synth.random_tree_batch(3, seed0=20240), 4000, None),
     "tree_deep": (lambda: synth.random_tree_cell(77, ncomp=400, max_levels=40), 2000, None),
+    # event-driven network: ExpSyn/Exp2Syn, PreSyn detection, NetCon delays, NetStims (noise 1)
+    "net_spiking": (lambda: synth.spiking_network(nstim=6, weight=(0.02, 0.08), stim_noise=1.0, stim_interval=5.0),
+                    2400, None),
+    # HalfGap + gapjunction_lr + neuron_to_neuron_syn_lr coupling
+    "net_coupled": (lambda: synth.coupled_network(), 2000, None),
 }
 
 

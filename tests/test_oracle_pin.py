@@ -33,9 +33,15 @@ def test_oracle_bit_exact_vs_reference_golden(path):
     make, nstep, _ = _mg.CASES[name]
     d = np.load(path)
     g = make()
-    tr, _ = O.forward(g, int(d["nstep"]), probe=d["probes"])
+    tr, st = O.forward(g, int(d["nstep"]), probe=d["probes"])
     assert tr.shape == d["trace"].shape
     assert np.array_equal(tr, d["trace"]), np.max(np.abs(tr - d["trace"]))
+    if g.has_network:
+        # spk.dat holds times with 8 significant digits, sorted by (time, gid)
+        mine = sorted(st["spikes"])
+        ref = [tuple(r) for r in d["spikes"]]
+        assert [gid for _, gid in mine] == [int(gid) for _, gid in ref]
+        assert np.allclose([t for t, _ in mine], [t for t, _ in ref], rtol=1e-7, atol=1e-9)
 
 
 def test_golden_fixtures_present():
@@ -87,3 +93,60 @@ def test_adam_port_bit_exact_vs_reference_golden():
                            a["impedance"])
     assert np.array_equal(ws, d["weights"])
     assert np.array_equal(m, d["m"]) and np.array_equal(v, d["v"])
+
+
+@needs_ref
+@pytest.mark.parametrize("seed", [21, 22])
+def test_oracle_network_bit_exact_vs_reference_live(seed):
+    """Event network (ExpSyn, Exp2Syn, NetStims with noise 1) against the
+    reference's CPU mode, whose NetStim stream starts from a zeroed state."""
+    g = synth.spiking_network(ncell=6, seed=seed, nstim=5, weight=(0.02, 0.08), stim_noise=1.0, stim_interval=4.0)
+    p = np.arange(g.nnode, dtype=np.int32)[::11]
+    ref, rs = O.ref_forward(g, 2000, probe=p)
+    ora, st = O.forward(g, 2000, probe=p)
+    assert np.array_equal(ref, ora)
+    assert [gid for _, gid in sorted(st["spikes"])] == [gid for _, gid in rs]
+
+
+@needs_ref
+def test_oracle_coupled_bit_exact_vs_reference_live():
+    g = synth.coupled_network(ncell=5, seed=31, ngap=5, ngapj=4, ngraded=12)
+    p = np.arange(g.nnode, dtype=np.int32)[::9]
+    ref, _ = O.ref_forward(g, 2000, probe=p)
+    ora, _ = O.forward(g, 2000, probe=p)
+    assert np.array_equal(ref, ora)
+
+
+@needs_ref
+def test_network_adjoint_vs_fd_of_reference_forward():
+    """Weight / conductance gradients of the oracle adjoint against 4th-order FD of
+    the reference forward (event schedule unchanged by the small steps)."""
+    T = 800
+    rng = np.random.default_rng(5)
+    cases = (
+        (synth.spiking_network(ncell=4, seed=3, nstim=2, weight=(0.02, 0.06)),
+         (("exp2syn", "weight", "Exp2Syn.weight"), ("expsyn", "weight", "ExpSyn.weight"))),
+        (synth.coupled_network(ncell=4, seed=8, ngap=3, ngapj=2, ngraded=5),
+         (("halfgap", "g", "HalfGap.g"), ("gapjunction", "w", "gapjunction_lr.w"),
+          ("graded", "w", "neuron_to_neuron_syn_lr.w"))),
+    )
+    for g, checks in cases:
+        p = g.soma_nodes()
+        c = rng.standard_normal((T + 1, p.shape[0]))
+        _, gr = O.adjoint(g, T, c, probe=p)
+
+        def L(gg):
+            return float(np.sum(c * O.ref_forward(gg, T, probe=p)[0]))
+
+        for tab, field, key in checks:
+            t = getattr(g, tab)
+            j = int(np.argmax(np.abs(gr[key])))
+            x0 = t.fields[field][j]
+            h = 1e-3 * abs(x0)
+            vals = []
+            for dx in (2 * h, h, -h, -2 * h):
+                gg = g.copy()
+                getattr(gg, tab).fields[field][j] = x0 + dx
+                vals.append(L(gg))
+            fd = (-vals[0] + 8 * vals[1] - 8 * vals[2] + vals[3]) / (12 * h)
+            assert abs(gr[key][j] - fd) <= 1e-6 * abs(fd), (key, gr[key][j], fd)
