@@ -26,8 +26,16 @@ HX_P = {
     "pas.e": 5,
     "cm": 6,
     "IClamp.amp": 7,
+    "ExpSyn.weight": 8,
+    "ExpSyn.e": 9,
+    "Exp2Syn.weight": 10,
+    "Exp2Syn.e": 11,
+    "HalfGap.g": 12,
+    "gapjunction_lr.g": 13,
+    "gapjunction_lr.w": 14,
+    "neuron_to_neuron_syn_lr.w": 15,
 }
-HX_P_COUNT = 8
+HX_P_COUNT = 16
 
 
 class GroupDesc(C.Structure):
@@ -58,7 +66,23 @@ class GroupDesc(C.Structure):
         ("ic_del", _dp),
         ("ic_dur", _dp),
         ("ic_amp", _dp),
+        ("gid_base", C.c_int), ("nsrc_cells", C.c_int),
+        ("ps_thresh", _dp),
+        ("nexpsyn", C.c_int), ("expsyn_node", _ip), ("expsyn_src", _ip),
+        ("expsyn_tau", _dp), ("expsyn_e", _dp), ("expsyn_delay", _dp), ("expsyn_weight", _dp),
+        ("nexp2syn", C.c_int), ("exp2syn_node", _ip), ("exp2syn_src", _ip),
+        ("exp2syn_tau1", _dp), ("exp2syn_tau2", _dp), ("exp2syn_e", _dp), ("exp2syn_delay", _dp),
+        ("exp2syn_weight", _dp),
+        ("nnetstim", C.c_int), ("ns_interval", _dp), ("ns_number", _dp), ("ns_start", _dp), ("ns_noise", _dp),
+        ("netstim_rng", C.c_int),
+        ("nhalfgap", C.c_int), ("hg_node", _ip), ("hg_src", _ip), ("hg_g", _dp),
+        ("ngapj", C.c_int), ("gj_node", _ip), ("gj_pre", _ip), ("gj_g", _dp), ("gj_w", _dp),
+        ("ngraded", C.c_int), ("gr_node", _ip), ("gr_pre", _ip), ("gr_w", _dp), ("gr_delta", _dp), ("gr_vth", _dp),
     ]
+
+
+# int (*)(void* user, const void* send_dev, void* recv_dev, int cap_entries, void* stream)
+EXCHANGE_FN = C.CFUNCTYPE(C.c_int, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_void_p)
 
 
 class PlanStats(C.Structure):
@@ -111,6 +135,11 @@ SIGNATURES = {
     "hx_opt_get_adam_state": (C.c_int, [C.c_void_p, C.c_int, C.POINTER(C.c_longlong), _dp, _dp, C.c_int, _dp]),
     "hx_opt_set_adam_state": (C.c_int, [C.c_void_p, C.c_int, C.c_longlong, _dp, _dp, C.c_int, _dp]),
     "hx_opt_reset": (C.c_int, [C.c_void_p, C.c_int]),
+    "hx_get_spikes": (C.c_int, [C.c_void_p, C.c_int, _ip, _dp, _ip]),
+    "hx_netstim_trains": (C.c_int, [C.POINTER(GroupDesc), C.c_int, C.c_int, _ip, _ip, _ip]),
+    "hx_set_exchange": (C.c_int, [C.c_void_p, EXCHANGE_FN, C.c_void_p, C.c_int]),
+    "hx_set_window": (C.c_int, [C.c_void_p, C.c_int]),
+    "hx_get_window": (C.c_int, [C.c_void_p, _ip]),
 }
 
 _LIB = None
@@ -145,9 +174,13 @@ def fptr(x: np.ndarray):
 
 
 class BoundGroup:
-    """A GroupDesc pointing at contiguous numpy copies of a CellGroup's arrays."""
+    """A GroupDesc pointing at contiguous numpy copies of a CellGroup's arrays.
 
-    def __init__(self, g):
+    ``gid_base`` / ``nsrc_cells``: this group's first global cell id and the
+    number of cells over all groups of a multi-GPU job (0 = the group alone).
+    """
+
+    def __init__(self, g, gid_base: int = 0, nsrc_cells: int = 0):
         self.keep = []
 
         def D(x):
@@ -178,7 +211,49 @@ class BoundGroup:
         s.nic = c.n
         s.ic_node = I(c.nodes)
         s.ic_del, s.ic_dur, s.ic_amp = D(c.fields["del"]), D(c.fields["dur"]), D(c.fields["amp"])
+        # network parts (all empty for a group without them)
+        s.gid_base = int(gid_base)
+        s.nsrc_cells = int(nsrc_cells) if nsrc_cells else g.ncell
+        s.ps_thresh = D(g.ps_thresh) if g.has_network else _dp()
+        e1, e2 = g.expsyn, g.exp2syn
+        s.nexpsyn, s.expsyn_node, s.expsyn_src = e1.n, I(e1.nodes), I(e1.ifields["src"])
+        s.expsyn_tau, s.expsyn_e, s.expsyn_delay, s.expsyn_weight = (
+            D(e1.fields[k]) for k in ("tau", "e", "delay", "weight"))
+        s.nexp2syn, s.exp2syn_node, s.exp2syn_src = e2.n, I(e2.nodes), I(e2.ifields["src"])
+        s.exp2syn_tau1, s.exp2syn_tau2, s.exp2syn_e, s.exp2syn_delay, s.exp2syn_weight = (
+            D(e2.fields[k]) for k in ("tau1", "tau2", "e", "delay", "weight"))
+        ns = g.netstim
+        s.nnetstim = ns.n
+        s.ns_interval, s.ns_number, s.ns_start, s.ns_noise = (
+            D(ns.fields[k]) for k in ("interval", "number", "start", "noise"))
+        s.netstim_rng = int(g.netstim_rng)
+        hg = g.halfgap
+        s.nhalfgap, s.hg_node, s.hg_src, s.hg_g = hg.n, I(hg.nodes), I(hg.ifields["src"]), D(hg.fields["g"])
+        gj = g.gapjunction
+        s.ngapj, s.gj_node, s.gj_pre = gj.n, I(gj.nodes), I(gj.ifields["pre"])
+        s.gj_g, s.gj_w = D(gj.fields["g"]), D(gj.fields["w"])
+        gr = g.graded
+        s.ngraded, s.gr_node, s.gr_pre = gr.n, I(gr.nodes), I(gr.ifields["pre"])
+        s.gr_w, s.gr_delta, s.gr_vth = D(gr.fields["w"]), D(gr.fields["delta"]), D(gr.fields["Vth"])
         self.desc = s
+
+
+def netstim_trains(g, nstep: int):
+    """NetStim spike trains of ``g`` from the native host generator (no GPU):
+    arrays (instance, step) in emission order."""
+    L = load()
+    b = BoundGroup(g)
+    n = C.c_int(0)
+    rc = L.hx_netstim_trains(C.byref(b.desc), int(nstep), 0, _ip(), _ip(), C.byref(n))
+    if rc != 0:
+        raise ValueError("hx_netstim_trains failed")
+    cap = int(n.value)
+    ids = np.zeros(max(cap, 1), dtype=np.int32)
+    steps = np.zeros(max(cap, 1), dtype=np.int32)
+    rc = L.hx_netstim_trains(C.byref(b.desc), int(nstep), cap, iptr(ids), iptr(steps), C.byref(n))
+    if rc != 0:
+        raise ValueError("hx_netstim_trains failed")
+    return ids[:cap], steps[:cap]
 
 
 def plan_check(g, nodes_per_pack: int = 0):

@@ -49,15 +49,63 @@ struct DevProbe {
     int nprobe;
 };
 
-// Adjoint state (between windows), node-indexed.
+// Adjoint state (between windows), node-indexed; lA/lB per synapse.
 struct DevAdj {
     double *lv, *lm, *lh, *ln;
+    double *lA, *lB;
 };
 
-// Gradient accumulators: node-indexed except ic_amp (per IClamp instance).
+// Gradient accumulators: node-indexed except ic_amp (per IClamp instance)
+// and the network kinds (per instance in GPU order).
 struct DevGrad {
     double *hh_gnabar, *hh_gkbar, *hh_gl, *hh_el;
     double *pas_g, *pas_e, *cm, *ic_amp;
+    double *syn_w, *syn_e;             // exponential synapses (ExpSyn then Exp2Syn per node)
+    double *hg_g, *gj_g, *gj_w, *gr_w;  // HalfGap, gapjunction_lr, neuron_to_neuron_syn_lr
+};
+
+// Network parts of a group (step kernels instantiated with kNet = true).
+// Instance arrays are in GPU order: sorted by GPU node, ExpSyn before Exp2Syn
+// on a node, then by reference instance -- the order in which the reference's
+// mechanism loop accumulates them into one node's rhs/d.
+struct DevNet {
+    // exponential synapses: B' = B + fB w, A' = A + fA w at an event;
+    // x <- x + c (0 - x) per step (c = 1 - exp(-dt/tau)); i = (B - A)(v - e)
+    int nsyn, smem_syn;
+    const int *node_syn_off, *pack_syn_off;
+    const double *syn_e, *syn_w, *syn_cA, *syn_cB, *syn_fA, *syn_fB;
+    double *sA, *sB;  // state between windows
+    double *tA, *tB;  // tape rows (k - k_base) x nsyn after the step's deliveries; null = no tape
+    // events: bucket k holds the synapses that receive an event at step k
+    const int *ev_cnt, *ev_syn;
+    int ev_cap;
+    // PreSyn threshold detection (one per cell slot; -1: none)
+    const int *cs_ps_node, *cs_gid;
+    const double* cs_ps_thr;
+    int* cs_ps_flag;
+    int2* win_spk;  // (source gid, step) of the window's spikes
+    int* win_n;
+    int win_cap, detect;
+    // HalfGap (electrode): i = (v[src] - v) g
+    const int *node_hg_off, *hg_src;
+    const double* hg_g;
+    // gapjunction_lr: i = w (g (v - v[pre]))
+    const int *node_gj_off, *gj_pre;
+    const double *gj_g, *gj_w;
+    // neuron_to_neuron_syn_lr: i = |w| (g s (v - erev)), s' = inf + (s - inf) exp(-dt/tau)
+    const int *node_gr_off, *gr_pre;
+    const double *gr_w, *gr_g, *gr_k, *gr_erev, *gr_delta, *gr_vth;
+    int ngr;
+    double *gr_s, *lS;  // state s (s_{k-1} entering step k), adjoint of s
+    double* tS;         // tape: row 0 = s_{k_base-1}, row k-k_base+1 = s_k
+    int coupled;             // gaps or graded synapses present: one step per launch
+    const double* vpeer;     // v_k of every node (read-only during a coupled launch)
+    double* vout;            // v_{k+1} written by a coupled forward launch
+    // reverse-sweep coupling: per-instance contributions to the partner's
+    // dL/dv, written by the launch of step k, read by the launch of step k-1
+    double *x_hg_out, *x_gj_out, *x_gr_out;
+    const double *x_hg_in, *x_gj_in, *x_gr_in;
+    const int *node_in_off, *node_in;  // incoming (kind << 28 | instance) per node
 };
 
 }  // namespace hx

@@ -142,6 +142,7 @@ struct Grp {
     int tl, nt;      // thread index inside the group, group size
     int bar, nwarp;  // named barrier id (multi-warp groups)
     int lvl, nlev;   // offset of the cell's level table in Meta::lvl, levels
+    int slot;        // global cell-slot index
     __device__ __forceinline__ void sync() const {
         if (nwarp == 1)
             __syncwarp();
@@ -200,6 +201,7 @@ __device__ __forceinline__ bool setup_pack(const DevGroup& G, int p, int* ibase,
             g.tl = tid - 32 * w0;
             g.nt = 32 * nw;
             g.bar = G.cs_bar[s];
+            g.slot = s;
             g.nwarp = nw;
             g.lvl = G.cs_lvl_off[s] - l0;
             g.nlev = G.cs_nlev[s];
@@ -261,13 +263,64 @@ __device__ __forceinline__ void hines_cell(const Meta& M, const Grp& g, const do
 }
 
 // ------------------------------------------------------------------ assembly
+// One point-process contribution through MechTemp::current
+// (mech_template.cuh:612-645): i1 = I(v+0.001), i0 = I(v), scaled by 1e2/area.
+__device__ __forceinline__ void pp_add(double i1, double i0, double area, bool electrode, double& r, double& dd) {
+    double gg = (i1 - i0) * kInvFdEps;
+    gg *= 1.e2 / area;
+    i0 *= 1.e2 / area;
+    if (electrode) {
+        r += i0;
+        dd -= gg;
+    } else {
+        r -= i0;
+        dd += gg;
+    }
+}
+
+// Network currents of GPU node gi after IClamp, in the exported mechanism
+// order: ExpSyn, Exp2Syn (expsyn.cpp:92-121, exp2syn_temp.cuh:45-49), HalfGap
+// (HalfGap.cu:56-62, electrode), gapjunction_lr (gapjunction_lr.cu:58-65),
+// neuron_to_neuron_syn_lr (neuron_to_neuron_syn_lr.cu:120-127).  synA/synB are
+// the cell's synapse states indexed from syn0; grs the graded states s_k.
+__device__ __forceinline__ void assemble_net(const DevGroup& G, const DevNet& N, int gi, double vi,
+                                             const double* __restrict__ synA, const double* __restrict__ synB,
+                                             int syn0, const double* __restrict__ grs,
+                                             const double* __restrict__ vpeer, double& r, double& dd) {
+    const double area = __ldg(G.area + gi);
+    const int s1 = __ldg(N.node_syn_off + gi + 1);
+    for (int j = __ldg(N.node_syn_off + gi); j < s1; ++j) {
+        const double gs = synB[j - syn0] - synA[j - syn0], e = __ldg(N.syn_e + j);
+        pp_add(gs * ((vi + kFdEps) - e), gs * (vi - e), area, false, r, dd);
+    }
+    if (!N.coupled) return;
+    const int h1 = __ldg(N.node_hg_off + gi + 1);
+    for (int j = __ldg(N.node_hg_off + gi); j < h1; ++j) {
+        const double vg = vpeer[__ldg(N.hg_src + j)], g = __ldg(N.hg_g + j);
+        pp_add((vg - (vi + kFdEps)) * g, (vg - vi) * g, area, true, r, dd);
+    }
+    const int j1 = __ldg(N.node_gj_off + gi + 1);
+    for (int j = __ldg(N.node_gj_off + gi); j < j1; ++j) {
+        const double vp = vpeer[__ldg(N.gj_pre + j)], g = __ldg(N.gj_g + j), w = __ldg(N.gj_w + j);
+        pp_add(w * (g * ((vi + kFdEps) - vp)), w * (g * (vi - vp)), area, false, r, dd);
+    }
+    const int r1 = __ldg(N.node_gr_off + gi + 1);
+    for (int j = __ldg(N.node_gr_off + gi); j < r1; ++j) {
+        const double aw = fabs(__ldg(N.gr_w + j)), gs = __ldg(N.gr_g + j) * grs[j], er = __ldg(N.gr_erev + j);
+        pp_add(aw * (gs * ((vi + kFdEps) - er)), aw * (gs * (vi - er)), area, false, r, dd);
+    }
+}
+
 // rhs/d of pack-local node i in the reference's accumulation order:
-// pas, hh, IClamp (CoreNEURON type order), capacitance jacobian, axial terms.
-template <bool kRhs>
+// pas, hh, IClamp (CoreNEURON type order), [network currents], capacitance
+// jacobian, axial terms.
+template <bool kRhs, bool kNet = false>
 __device__ __forceinline__ void assemble(const DevGroup& G, const Meta& M, int pb, int i, int fl,
                                          const double* __restrict__ sv, const double* __restrict__ sa,
                                          const double* __restrict__ sb, double m, double h, double n, double tmid,
-                                         double& r_out, double& d_out) {
+                                         double& r_out, double& d_out, const DevNet& N = DevNet{},
+                                         const double* synA = nullptr, const double* synB = nullptr, int syn0 = 0,
+                                         const double* grs = nullptr, const double* vpeer = nullptr) {
     const int gi = pb + i;
     const double vi = sv[i];
     double r = 0.0, dd = 0.0;
@@ -295,6 +348,7 @@ __device__ __forceinline__ void assemble(const DevGroup& G, const Meta& M, int p
         const double cur = (tmid < del + dur && tmid >= del) ? __ldg(G.ic_amp + j) : 0.0;
         r += cur * (1.e2 / __ldg(G.area + gi));
     }
+    if (kNet) assemble_net(G, N, gi, vi, synA, synB, syn0, grs, vpeer, r, dd);
     dd += G.cfac * __ldg(G.cm + gi);
     const int par = M.par[i];
     if (par >= 0) {
@@ -331,23 +385,36 @@ __global__ void init_state_kernel(DevGroup G, DevState S, double v_init) {
 }
 
 // ------------------------------------------------------------------ forward
+// kNet adds, per step: PreSyn threshold detection at the step's start
+// (PreSyn::threshold_detect_cpu, presyn.cpp:133-177: a spike at t_k when
+// v > threshold and the hysteresis flag is clear), delivery of the step's
+// events from bucket k (net_receive: A += w*fA, B += w*fB; the reference's
+// delivery condition deliver_time <= t + dt/2 is resolved into the bucket
+// index when an event is routed), the network currents and the synapse /
+// graded-synapse state updates.  In a coupled launch (gaps, graded
+// synapses; one step) partner voltages come from N.vpeer and v_{k+1} goes to
+// N.vout, so that no CTA reads a value another CTA rewrites.
+template <bool kNet>
 __global__ void __launch_bounds__(kThreads, 2) fwd_kernel(DevGroup G, DevState S, DevTape T, int write_tape,
                                                            DevProbe P, double* __restrict__ trace,
-                                                           const double* __restrict__ tmid, int k0, int k1) {
+                                                           const double* __restrict__ tmid, int k0, int k1, DevNet N) {
     extern __shared__ double smem[];
     const int p = blockIdx.x;
-    const int N = G.smem_n;
+    const int N_ = G.smem_n;
     double* sv = smem;
-    double* srhs = sv + N;
-    double* sd = srhs + N;
-    double* sa = sd + N;
-    double* sb = sa + N;
-    double* sgm = sb + N;
-    double* sgh = sgm + N;
-    double* sgn = sgh + N;
+    double* srhs = sv + N_;
+    double* sd = srhs + N_;
+    double* sa = sd + N_;
+    double* sb = sa + N_;
+    double* sgm = sb + N_;
+    double* sgh = sgm + N_;
+    double* sgn = sgh + N_;
+    double* ssA = sgn + N_;                       // kNet: synapse states of the pack
+    double* ssB = ssA + (kNet ? N.smem_syn : 0);
+    double* send = ssB + (kNet ? N.smem_syn : 0);
     Meta M;
     Grp g;
-    if (!setup_pack(G, p, reinterpret_cast<int*>(sgn + N), M, g)) return;
+    if (!setup_pack(G, p, reinterpret_cast<int*>(send), M, g)) return;
     const int pb = G.pack_node_off[p];
     const int i0 = g.nb, i1 = g.nb + g.n;
     for (int i = i0 + g.tl; i < i1; i += g.nt) {
@@ -357,6 +424,24 @@ __global__ void __launch_bounds__(kThreads, 2) fwd_kernel(DevGroup G, DevState S
         sgm[i] = S.m[pb + i];
         sgh[i] = S.h[pb + i];
         sgn[i] = S.n[pb + i];
+    }
+    // kNet: the cell's synapses [c0, c1) (global ids), stored from ps0 in shared memory
+    int c0 = 0, c1 = 0, ps0 = 0, psnode = -1, psflag = 0, gid = 0;
+    double psthr = 0.0;
+    if (kNet) {
+        ps0 = N.pack_syn_off[p];
+        c0 = N.node_syn_off[pb + i0];
+        c1 = N.node_syn_off[pb + i1];
+        for (int j = c0 + g.tl; j < c1; j += g.nt) {
+            ssA[j - ps0] = N.sA[j];
+            ssB[j - ps0] = N.sB[j];
+        }
+        psnode = N.cs_ps_node[g.slot];
+        if (psnode >= 0) {
+            psflag = N.cs_ps_flag[g.slot];
+            psthr = N.cs_ps_thr[g.slot];
+            gid = N.cs_gid[g.slot];
+        }
     }
     const int q0 = P.pack_off[p], q1 = P.pack_off[p + 1];
     g.sync();
@@ -375,11 +460,62 @@ __global__ void __launch_bounds__(kThreads, 2) fwd_kernel(DevGroup G, DevState S
                 T.n[off + i] = sgn[i];
             }
         }
+        if (kNet) {
+            if (N.detect && g.tl == 0 && psnode >= 0) {
+                const double pv = sv[psnode];
+                if (pv > psthr && !psflag) {
+                    const int q = atomicAdd(N.win_n, 1);
+                    if (q < N.win_cap) N.win_spk[q] = make_int2(gid, k);
+                    psflag = 1;
+                } else if (pv <= psthr) {
+                    psflag = 0;
+                }
+            }
+            const int cnt = min(N.ev_cnt[k], N.ev_cap);
+            const int* ev = N.ev_syn + (size_t)k * N.ev_cap;
+            for (int e = g.tl; e < cnt; e += g.nt) {
+                const int j = ev[e];
+                if (j >= c0 && j < c1) {
+                    const double w = __ldg(N.syn_w + j);
+                    atomicAdd(ssA + (j - ps0), w * __ldg(N.syn_fA + j));
+                    atomicAdd(ssB + (j - ps0), w * __ldg(N.syn_fB + j));
+                }
+            }
+            g.sync();
+            if (N.tA) {
+                const size_t off = (size_t)(k - T.k_base) * (size_t)N.nsyn;
+                for (int j = c0 + g.tl; j < c1; j += g.nt) {
+                    N.tA[off + j] = ssA[j - ps0];
+                    N.tB[off + j] = ssB[j - ps0];
+                }
+            }
+        }
         const double tm = tmid[k];
         // A: assembly
         for (int i = i0 + g.tl; i < i1; i += g.nt) {
             double r, dd;
-            assemble<true>(G, M, pb, i, M.flag[i], sv, sa, sb, sgm[i], sgh[i], sgn[i], tm, r, dd);
+            if (kNet) {
+                const int gi = pb + i;
+                if (N.coupled) {  // graded synapses: s_k from s_{k-1} and vpre_k (deferred cnexp update)
+                    const int r1 = __ldg(N.node_gr_off + gi + 1);
+                    for (int j = __ldg(N.node_gr_off + gi); j < r1; ++j) {
+                        double sj = N.gr_s[j];
+                        if (write_tape && k == T.k_base) N.tS[(size_t)j] = sj;  // row 0: s_{k_base - 1}
+                        if (k > 0) {
+                            const double vpre = N.vpeer[__ldg(N.gr_pre + j)];
+                            const double inf = 1.0 / (1.0 + exp((__ldg(N.gr_vth + j) - vpre) / __ldg(N.gr_delta + j)));
+                            const double tau = (1.0 - inf) / __ldg(N.gr_k + j);
+                            sj = inf + (sj - inf) * exp(-G.dt / tau);
+                            N.gr_s[j] = sj;
+                        }
+                        if (write_tape) N.tS[(size_t)(k - T.k_base + 1) * N.ngr + j] = sj;
+                    }
+                }
+                assemble<true, true>(G, M, pb, i, M.flag[i], sv, sa, sb, sgm[i], sgh[i], sgn[i], tm, r, dd, N, ssA,
+                                     ssB, ps0, N.gr_s, N.vpeer);
+            } else {
+                assemble<true>(G, M, pb, i, M.flag[i], sv, sa, sb, sgm[i], sgh[i], sgn[i], tm, r, dd);
+            }
             srhs[i] = r;
             sd[i] = dd;
         }
@@ -397,6 +533,14 @@ __global__ void __launch_bounds__(kThreads, 2) fwd_kernel(DevGroup G, DevState S
                 sgh[i] = gate_step(sgh[i], r.inf[1], r.k[1], G.dt);
                 sgn[i] = gate_step(sgn[i], r.inf[2], r.k[2], G.dt);
             }
+            if (kNet) {  // synapse decay x + c (0 - x) (expsyn.cpp:125-134, exp2syn_temp.cuh:51-58)
+                const int s1 = __ldg(N.node_syn_off + pb + i + 1);
+                for (int j = __ldg(N.node_syn_off + pb + i); j < s1; ++j) {
+                    const double A = ssA[j - ps0], B = ssB[j - ps0];
+                    ssA[j - ps0] = A + __ldg(N.syn_cA + j) * (0.0 - A);
+                    ssB[j - ps0] = B + __ldg(N.syn_cB + j) * (0.0 - B);
+                }
+            }
         }
         g.sync();
         if (trace)
@@ -409,11 +553,19 @@ __global__ void __launch_bounds__(kThreads, 2) fwd_kernel(DevGroup G, DevState S
         const size_t off = (size_t)(k1 - T.k_base) * (size_t)G.nnode + pb;
         for (int i = i0 + g.tl; i < i1; i += g.nt) T.v[off + i] = sv[i];
     }
+    double* vdst = (kNet && N.coupled) ? N.vout : S.v;
     for (int i = i0 + g.tl; i < i1; i += g.nt) {
-        S.v[pb + i] = sv[i];
+        vdst[pb + i] = sv[i];
         S.m[pb + i] = sgm[i];
         S.h[pb + i] = sgh[i];
         S.n[pb + i] = sgn[i];
+    }
+    if (kNet) {
+        for (int j = c0 + g.tl; j < c1; j += g.nt) {
+            N.sA[j] = ssA[j - ps0];
+            N.sB[j] = ssB[j - ps0];
+        }
+        if (g.tl == 0 && psnode >= 0) N.cs_ps_flag[g.slot] = psflag;
     }
 }
 
@@ -421,41 +573,70 @@ __global__ void __launch_bounds__(kThreads, 2) fwd_kernel(DevGroup G, DevState S
 // Reverse sweep over steps [k_lo, k_hi).  Per step k, with lv = dL/dv_{k+1}
 // and lm/lh/ln = dL/d(gates_{k+1}):
 //   S  gates_{k+1} = E*gates_k + (1-E)*inf(v_{k+1}), E = exp(-dt k(v_{k+1})):
-//      mu = lv + sum lg*dgate'/dv', lg *= E;
+//      mu = lv + sum lg*dgate'/dv', lg *= E;  synapse states: lx *= 1 - c;
 //   A  recompute the diagonal d_k (FD conductances at v_k, gates_k);
 //   B  w = M_k^{-T} mu (Hines with a and b swapped);
 //   V  lambda_d = -w*dv; VJPs of rhs_k and d_k into lv (dL/dv_k), the gate
-//      adjoints and the per-node parameter gradients.
+//      and synapse adjoints and the per-node parameter gradients; then the
+//      weight gradients of the step's events (A' = A + fA w, B' = B + fB w).
+// The FD conductance expressions are differentiated as the functions of the
+// parameters they are (for currents linear in v their v-derivative is 0).
+// Coupled launches (one step): the dL/dv_k contributions of a gap or graded
+// synapse to its partner node go through N.x_*_out and are gathered by the
+// launch of step k-1 from N.x_*_in, in the fixed order of N.node_in.
+template <bool kNet>
 __global__ void __launch_bounds__(kThreads, 2) bwd_kernel(DevGroup G, DevTape T, DevAdj Ad, DevGrad GR, DevProbe P,
                                                            const double* __restrict__ dLdv,
-                                                           const double* __restrict__ tmid, int k_hi, int k_lo) {
+                                                           const double* __restrict__ tmid, int k_hi, int k_lo,
+                                                           DevNet N) {
     extern __shared__ double smem[];
     const int p = blockIdx.x;
-    const int N = G.smem_n;
+    const int N_ = G.smem_n;
     double* slv = smem;
-    double* sw = slv + N;
-    double* sd = sw + N;
-    double* sa = sd + N;
-    double* sb = sa + N;
-    double* svk = sb + N;
-    double* svk1 = svk + N;
-    double* slm = svk1 + N;
-    double* slh = slm + N;
-    double* sln = slh + N;
+    double* sw = slv + N_;
+    double* sd = sw + N_;
+    double* sa = sd + N_;
+    double* sb = sa + N_;
+    double* svk = sb + N_;
+    double* svk1 = svk + N_;
+    double* slm = svk1 + N_;
+    double* slh = slm + N_;
+    double* sln = slh + N_;
+    double* slA = sln + N_;  // kNet: synapse adjoints of the pack
+    double* slB = slA + (kNet ? N.smem_syn : 0);
+    double* send = slB + (kNet ? N.smem_syn : 0);
     Meta M;
     Grp g;
-    if (!setup_pack(G, p, reinterpret_cast<int*>(sln + N), M, g)) return;
+    if (!setup_pack(G, p, reinterpret_cast<int*>(send), M, g)) return;
     const int pb = G.pack_node_off[p];
     const int i0 = g.nb, i1 = g.nb + g.n;
     const double dt = G.dt, q10 = G.q10;
     for (int i = i0 + g.tl; i < i1; i += g.nt) {
-        slv[i] = Ad.lv[pb + i];
+        double l = Ad.lv[pb + i];
+        if (kNet && N.coupled) {  // partner contributions to dL/dv_{k_hi} from the launch of step k_hi
+            const int e1 = __ldg(N.node_in_off + pb + i + 1);
+            for (int e = __ldg(N.node_in_off + pb + i); e < e1; ++e) {
+                const int code = __ldg(N.node_in + e), kind = code >> 28, inst = code & 0x0FFFFFFF;
+                l += (kind == 0 ? N.x_hg_in : kind == 1 ? N.x_gj_in : N.x_gr_in)[inst];
+            }
+        }
+        slv[i] = l;
         sa[i] = G.a[pb + i];
         sb[i] = G.b[pb + i];
         slm[i] = Ad.lm[pb + i];
         slh[i] = Ad.lh[pb + i];
         sln[i] = Ad.ln[pb + i];
         svk1[i] = T.v[(size_t)(k_hi - T.k_base) * (size_t)G.nnode + pb + i];
+    }
+    int c0 = 0, c1 = 0, ps0 = 0;
+    if (kNet) {
+        ps0 = N.pack_syn_off[p];
+        c0 = N.node_syn_off[pb + i0];
+        c1 = N.node_syn_off[pb + i1];
+        for (int j = c0 + g.tl; j < c1; j += g.nt) {
+            slA[j - ps0] = Ad.lA[j];
+            slB[j - ps0] = Ad.lB[j];
+        }
     }
     const int q0 = P.pack_off[p], q1 = P.pack_off[p + 1];
     g.sync();
@@ -469,6 +650,10 @@ __global__ void __launch_bounds__(kThreads, 2) bwd_kernel(DevGroup G, DevTape T,
             }
         g.sync();
         const double tm = tmid[k];
+        const double* tA = kNet ? N.tA + (size_t)(k - T.k_base) * (size_t)N.nsyn : nullptr;
+        const double* tB = kNet ? N.tB + (size_t)(k - T.k_base) * (size_t)N.nsyn : nullptr;
+        const double* grs = (kNet && N.coupled) ? N.tS + (size_t)(k - T.k_base + 1) * N.ngr : nullptr;
+        const double* vpeer = T.v + (size_t)(k - T.k_base) * (size_t)G.nnode;
         // S + A
         for (int i = i0 + g.tl; i < i1; i += g.nt) {
             double mu = slv[i];
@@ -494,7 +679,16 @@ __global__ void __launch_bounds__(kThreads, 2) bwd_kernel(DevGroup G, DevTape T,
                 sln[i] = lam[2];
             }
             double r, dd;
-            assemble<false>(G, M, pb, i, fl, svk, sa, sb, gm, gh, gn, tm, r, dd);
+            if (kNet) {
+                const int s1 = __ldg(N.node_syn_off + pb + i + 1);
+                for (int j = __ldg(N.node_syn_off + pb + i); j < s1; ++j) {
+                    slA[j - ps0] *= 1.0 - __ldg(N.syn_cA + j);
+                    slB[j - ps0] *= 1.0 - __ldg(N.syn_cB + j);
+                }
+                assemble<false, true>(G, M, pb, i, fl, svk, sa, sb, gm, gh, gn, tm, r, dd, N, tA, tB, 0, grs, vpeer);
+            } else {
+                assemble<false>(G, M, pb, i, fl, svk, sa, sb, gm, gh, gn, tm, r, dd);
+            }
             sd[i] = dd;
             sw[i] = mu;
             slv[i] = mu;
@@ -538,15 +732,82 @@ __global__ void __launch_bounds__(kThreads, 2) bwd_kernel(DevGroup G, DevTape T,
                 const double del = __ldg(G.ic_del + j), dur = __ldg(G.ic_dur + j);
                 if (tm < del + dur && tm >= del) GR.ic_amp[j] += w * (1.e2 / __ldg(G.area + gi));
             }
+            if (kNet) {
+                const double sarea = 1.e2 / __ldg(G.area + gi);
+                const int s1 = __ldg(N.node_syn_off + gi + 1);
+                for (int j = __ldg(N.node_syn_off + gi); j < s1; ++j) {
+                    const double Gs = tB[j] - tA[j], e = __ldg(N.syn_e + j);
+                    const double lG = sarea * (ld - w * (vk - e));
+                    slB[j - ps0] += lG;
+                    slA[j - ps0] -= lG;
+                    GR.syn_e[j] += w * sarea * Gs;
+                    lvn -= w * sarea * Gs;
+                }
+                if (N.coupled) {
+                    const int h1 = __ldg(N.node_hg_off + gi + 1);
+                    for (int j = __ldg(N.node_hg_off + gi); j < h1; ++j) {
+                        const int q = __ldg(N.hg_src + j);
+                        const double gg = __ldg(N.hg_g + j);
+                        GR.hg_g[j] += w * sarea * (vpeer[q] - vk) + ld * sarea;
+                        lvn -= w * sarea * gg;
+                        N.x_hg_out[j] = w * sarea * gg;
+                    }
+                    const int j1 = __ldg(N.node_gj_off + gi + 1);
+                    for (int j = __ldg(N.node_gj_off + gi); j < j1; ++j) {
+                        const int q = __ldg(N.gj_pre + j);
+                        const double gg = __ldg(N.gj_g + j), ww = __ldg(N.gj_w + j), dv = vk - vpeer[q];
+                        GR.gj_w[j] += -w * sarea * gg * dv + ld * sarea * gg;
+                        GR.gj_g[j] += -w * sarea * ww * dv + ld * sarea * ww;
+                        lvn -= w * sarea * ww * gg;
+                        N.x_gj_out[j] = w * sarea * ww * gg;
+                    }
+                    const int r1 = __ldg(N.node_gr_off + gi + 1);
+                    for (int j = __ldg(N.node_gr_off + gi); j < r1; ++j) {
+                        const double W = __ldg(N.gr_w + j), aw = fabs(W), gg = __ldg(N.gr_g + j);
+                        const double er = __ldg(N.gr_erev + j), sk = grs[j], dvr = vk - er;
+                        double ls = N.lS[j] - w * sarea * aw * gg * dvr + ld * sarea * aw * gg;
+                        const double sgn = (double)((W > 0) - (W < 0));
+                        GR.gr_w[j] += sgn * (-w * sarea * gg * sk * dvr + ld * sarea * gg * sk);
+                        lvn -= w * sarea * aw * gg * sk;
+                        // state map s_k = F(s_{k-1}, vpre_k): its vpre_k part goes to the
+                        // presynaptic node (gathered by the launch of step k-1)
+                        double x = 0.0;
+                        if (k > 0) {
+                            const double vpre = vpeer[__ldg(N.gr_pre + j)];
+                            const double dl = __ldg(N.gr_delta + j), kk = __ldg(N.gr_k + j);
+                            const double inf = 1.0 / (1.0 + exp((__ldg(N.gr_vth + j) - vpre) / dl));
+                            const double tau = (1.0 - inf) / kk;
+                            const double E = exp(-dt / tau);
+                            const double dinf = inf * (1.0 - inf) / dl;
+                            const double dE = (E == 0.0) ? 0.0 : E * (dt / (tau * tau)) * (-dinf / kk);
+                            const double sprev = N.tS[(size_t)(k - T.k_base) * N.ngr + j];
+                            x = ls * (dinf * (1.0 - E) + (sprev - inf) * dE);
+                            ls *= E;
+                        }
+                        N.x_gr_out[j] = x;
+                        N.lS[j] = ls;
+                    }
+                }
+            }
             GR.cm[gi] += ld * G.cfac;
             const int par = M.par[i];
             if (par >= 0) lvn += sb[i] * w - sa[i] * sw[par];
-            const int c1 = M.cho[i + 1];
-            for (int k2 = M.cho[i]; k2 < c1; ++k2) {
+            const int c1n = M.cho[i + 1];
+            for (int k2 = M.cho[i]; k2 < c1n; ++k2) {
                 const int c = M.ch[k2];
                 lvn += sa[c] * w - sb[c] * sw[c];
             }
             slv[i] = lvn;
+        }
+        if (kNet) {  // event weight gradients: dL/dw += fA lA' + fB lB' per delivery at step k
+            g.sync();
+            const int cnt = min(N.ev_cnt[k], N.ev_cap);
+            const int* ev = N.ev_syn + (size_t)k * N.ev_cap;
+            for (int e = g.tl; e < cnt; e += g.nt) {
+                const int j = ev[e];
+                if (j >= c0 && j < c1)
+                    atomicAdd(GR.syn_w + j, __ldg(N.syn_fA + j) * slA[j - ps0] + __ldg(N.syn_fB + j) * slB[j - ps0]);
+            }
         }
         double* tmp = svk1;
         svk1 = svk;
@@ -559,6 +820,11 @@ __global__ void __launch_bounds__(kThreads, 2) bwd_kernel(DevGroup G, DevTape T,
         Ad.lh[pb + i] = slh[i];
         Ad.ln[pb + i] = sln[i];
     }
+    if (kNet)
+        for (int j = c0 + g.tl; j < c1; j += g.nt) {
+            Ad.lA[j] = slA[j - ps0];
+            Ad.lB[j] = slB[j - ps0];
+        }
 }
 
 // ------------------------------------------------------------------ small kernels
@@ -691,13 +957,21 @@ cudaError_t launch_f32_to_f64(const float* a, double* b, int n, cudaStream_t st)
 static size_t meta_bytes(const DevGroup& G) {
     return sizeof(int) * (3 * (size_t)G.smem_n + 1 + G.smem_nch + 4 * (size_t)G.smem_br + 1 + G.smem_bch + G.smem_lvl);
 }
-size_t fwd_smem_bytes(const DevGroup& G) { return sizeof(double) * 8 * (size_t)G.smem_n + meta_bytes(G); }
-size_t bwd_smem_bytes(const DevGroup& G) { return sizeof(double) * 10 * (size_t)G.smem_n + meta_bytes(G); }
+size_t fwd_smem_bytes(const DevGroup& G, int smem_syn) {
+    return sizeof(double) * (8 * (size_t)G.smem_n + 2 * (size_t)smem_syn) + meta_bytes(G);
+}
+size_t bwd_smem_bytes(const DevGroup& G, int smem_syn) {
+    return sizeof(double) * (10 * (size_t)G.smem_n + 2 * (size_t)smem_syn) + meta_bytes(G);
+}
 
-cudaError_t configure_kernels(size_t smem_fwd, size_t smem_bwd) {
-    cudaError_t e = cudaFuncSetAttribute(fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_fwd);
+cudaError_t configure_kernels(size_t smem_fwd, size_t smem_bwd, size_t smem_fwd_net, size_t smem_bwd_net) {
+    cudaError_t e = cudaFuncSetAttribute(fwd_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_fwd);
     if (e != cudaSuccess) return e;
-    return cudaFuncSetAttribute(bwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_bwd);
+    e = cudaFuncSetAttribute(bwd_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_bwd);
+    if (e != cudaSuccess) return e;
+    e = cudaFuncSetAttribute(fwd_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_fwd_net);
+    if (e != cudaSuccess) return e;
+    return cudaFuncSetAttribute(bwd_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_bwd_net);
 }
 
 cudaError_t launch_init(const DevGroup& G, const DevState& S, double v_init, cudaStream_t st) {
@@ -706,14 +980,170 @@ cudaError_t launch_init(const DevGroup& G, const DevState& S, double v_init, cud
 }
 
 cudaError_t launch_fwd(const DevGroup& G, const DevState& S, const DevTape& T, int write_tape, const DevProbe& P,
-                       double* trace, const double* tmid, int k0, int k1, cudaStream_t st) {
-    fwd_kernel<<<G.npack, kThreads, fwd_smem_bytes(G), st>>>(G, S, T, write_tape, P, trace, tmid, k0, k1);
+                       double* trace, const double* tmid, int k0, int k1, cudaStream_t st, const DevNet* N) {
+    if (N)
+        fwd_kernel<true><<<G.npack, kThreads, fwd_smem_bytes(G, N->smem_syn), st>>>(G, S, T, write_tape, P, trace,
+                                                                                   tmid, k0, k1, *N);
+    else
+        fwd_kernel<false><<<G.npack, kThreads, fwd_smem_bytes(G, 0), st>>>(G, S, T, write_tape, P, trace, tmid, k0,
+                                                                          k1, DevNet{});
     return cudaGetLastError();
 }
 
 cudaError_t launch_bwd(const DevGroup& G, const DevTape& T, const DevAdj& A, const DevGrad& GR, const DevProbe& P,
-                       const double* dLdv, const double* tmid, int k_hi, int k_lo, cudaStream_t st) {
-    bwd_kernel<<<G.npack, kThreads, bwd_smem_bytes(G), st>>>(G, T, A, GR, P, dLdv, tmid, k_hi, k_lo);
+                       const double* dLdv, const double* tmid, int k_hi, int k_lo, cudaStream_t st, const DevNet* N) {
+    if (N)
+        bwd_kernel<true><<<G.npack, kThreads, bwd_smem_bytes(G, N->smem_syn), st>>>(G, T, A, GR, P, dLdv, tmid, k_hi,
+                                                                                   k_lo, *N);
+    else
+        bwd_kernel<false><<<G.npack, kThreads, bwd_smem_bytes(G, 0), st>>>(G, T, A, GR, P, dLdv, tmid, k_hi, k_lo,
+                                                                          DevNet{});
+    return cudaGetLastError();
+}
+
+// ---------------------------------------------------------------- network helpers
+// Per-synapse constants (GPU order).  kind 0 ExpSyn: c_B = 1 - exp(dt*(-1/tau)),
+// an event adds w to B (expsyn.cpp:125-149).  kind 1 Exp2Syn: tau1 clamped to
+// [1e-9, 0.9999] tau2, factor = 1/(exp(-tp/tau2) - exp(-tp/tau1)) at the
+// peak time tp, an event adds w*factor to A and B (exp2syn_temp.cuh:29-66).
+__global__ void syn_prep_kernel(int n, const int* __restrict__ kind, const double* __restrict__ tau1,
+                                const double* __restrict__ tau2, double dt, double* cA, double* cB, double* fA,
+                                double* fB) {
+    const int j = blockIdx.x * blockDim.x + threadIdx.x;
+    if (j >= n) return;
+    if (kind[j] == 0) {
+        const double tau = tau2[j];
+        cA[j] = 0.0;
+        cB[j] = 1. - exp(dt * ((-1.0) / tau));
+        fA[j] = 0.0;
+        fB[j] = 1.0;
+    } else {
+        double t1 = tau1[j];
+        const double t2 = tau2[j];
+        if (t1 / t2 > 0.9999) t1 = 0.9999 * t2;
+        if (t1 / t2 < 1e-9) t1 = t2 * 1e-9;
+        const double tp = (t1 * t2) / (t2 - t1) * log(t2 / t1);
+        const double f = 1.0 / (-exp(-tp / t1) + exp(-tp / t2));
+        cA[j] = 1.0 - exp(dt * (-1.0 / t1));
+        cB[j] = 1.0 - exp(dt * (-1.0 / t2));
+        fA[j] = f;
+        fB[j] = f;
+    }
+}
+
+// finitialize of the network state: synapse states 0 (expsyn.cpp:76-83,
+// exp2syn_temp.cuh:38-40); graded synapses s = inf(v_init) and the
+// sign-of-w parameter set of their INITIAL block (neuron_to_neuron_syn_lr.cu:
+// 102-118).
+__global__ void init_net_kernel(int nsyn, double* sA, double* sB, int ngr, const double* __restrict__ gr_w,
+                                const double* __restrict__ gr_vth, const double* __restrict__ gr_delta,
+                                double* gr_g, double* gr_k, double* gr_erev, double* gr_s, double v_init) {
+    const int j = blockIdx.x * blockDim.x + threadIdx.x;
+    if (j < nsyn) {
+        sA[j] = 0.0;
+        sB[j] = 0.0;
+    }
+    if (j < ngr) {
+        gr_s[j] = 1.0 / (1.0 + exp((gr_vth[j] - v_init) / gr_delta[j]));
+        const bool exc = gr_w[j] > 0.0;
+        gr_g[j] = exc ? 4.9 : 2.0;
+        gr_k[j] = exc ? 0.5 : 0.015000001;
+        gr_erev[j] = exc ? 30.0 : -70.0;
+    }
+}
+
+// Event routing: every spike (source gid, step j) reaches the local synapses
+// of its source; the delivery step is the first k >= j with
+// t_j + delay <= t_k + dt/2 (the reference's post_spike_receive condition,
+// postsyn.cpp:43-61, applied at the start of every step).  Events before
+// k_min (inside an already simulated window) set bit 1 of *err, a full bucket
+// bit 2; bucket counts keep counting past ev_cap so the needed size is known.
+__global__ void route_kernel(const int2* __restrict__ spk, const int* __restrict__ nspk_dev, int nspk_max,
+                             const int* __restrict__ src_off, const int* __restrict__ src_syn, int nsrc,
+                             const double* __restrict__ delay, const double* __restrict__ tstart, int nstep,
+                             double half_dt, int k_min, int* ev_cnt, int* ev_syn, int ev_cap, int* err) {
+    const int n = nspk_dev ? min(*nspk_dev, nspk_max) : nspk_max;
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
+        const int2 sp = spk[i];
+        if (sp.x < 0 || sp.x >= nsrc || sp.y < 0 || sp.y >= nstep) continue;
+        const double tj = tstart[sp.y];
+        const int e1 = src_off[sp.x + 1];
+        for (int e = src_off[sp.x]; e < e1; ++e) {
+            const int syn = src_syn[e];
+            const double td = tj + delay[syn];
+            int lo = sp.y, hi = nstep;  // first k in [lo, hi) with td <= tstart[k] + half_dt, else hi
+            while (lo < hi) {
+                const int mid = (lo + hi) >> 1;
+                if (td <= tstart[mid] + half_dt)
+                    hi = mid;
+                else
+                    lo = mid + 1;
+            }
+            if (lo >= nstep) continue;
+            if (lo < k_min) {
+                atomicOr(err, 1);
+                continue;
+            }
+            const int c = atomicAdd(ev_cnt + lo, 1);
+            if (c < ev_cap)
+                ev_syn[(size_t)lo * ev_cap + c] = syn;
+            else
+                atomicOr(err, 2);
+        }
+    }
+}
+
+// appends the window's spikes to the forward's spike log
+__global__ void log_append_kernel(const int2* __restrict__ win, const int* __restrict__ win_n, int win_cap,
+                                  int2* log, int* log_n, int log_cap, int* err) {
+    const int n = min(*win_n, win_cap);
+    if (*win_n > win_cap && threadIdx.x == 0 && blockIdx.x == 0) atomicOr(err, 4);
+    const int base = *log_n;
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x)
+        if (base + i < log_cap) log[base + i] = win[i];
+}
+
+__global__ void log_advance_kernel(const int* __restrict__ win_n, int win_cap, int* log_n) {
+    *log_n += min(*win_n, win_cap);
+}
+
+cudaError_t launch_syn_prep(int n, const int* kind, const double* tau1, const double* tau2, double dt, double* cA,
+                            double* cB, double* fA, double* fB, cudaStream_t st) {
+    if (n <= 0) return cudaSuccess;
+    syn_prep_kernel<<<(n + 255) / 256, 256, 0, st>>>(n, kind, tau1, tau2, dt, cA, cB, fA, fB);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_init_net(int nsyn, double* sA, double* sB, int ngr, const double* gr_w, const double* gr_vth,
+                            const double* gr_delta, double* gr_g, double* gr_k, double* gr_erev, double* gr_s,
+                            double v_init, cudaStream_t st) {
+    const int n = nsyn > ngr ? nsyn : ngr;
+    if (n <= 0) return cudaSuccess;
+    init_net_kernel<<<(n + 255) / 256, 256, 0, st>>>(nsyn, sA, sB, ngr, gr_w, gr_vth, gr_delta, gr_g, gr_k, gr_erev,
+                                                     gr_s, v_init);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_route(const int2* spk, const int* nspk_dev, int nspk_max, const int* src_off, const int* src_syn,
+                         int nsrc, const double* delay, const double* tstart, int nstep, double half_dt, int k_min,
+                         int* ev_cnt, int* ev_syn, int ev_cap, int* err, cudaStream_t st) {
+    if (nspk_max <= 0) return cudaSuccess;
+    int blocks = (nspk_max + 255) / 256;
+    if (blocks > 4 * 148) blocks = 4 * 148;
+    route_kernel<<<blocks, 256, 0, st>>>(spk, nspk_dev, nspk_max, src_off, src_syn, nsrc, delay, tstart, nstep,
+                                         half_dt, k_min, ev_cnt, ev_syn, ev_cap, err);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_log_append(const int2* win, const int* win_n, int win_cap, int2* log, int* log_n, int log_cap,
+                              int* err, cudaStream_t st) {
+    int blocks = (win_cap + 255) / 256;
+    if (blocks > 148) blocks = 148;
+    if (blocks < 1) blocks = 1;
+    log_append_kernel<<<blocks, 256, 0, st>>>(win, win_n, win_cap, log, log_n, log_cap, err);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+    log_advance_kernel<<<1, 1, 0, st>>>(win_n, win_cap, log_n);
     return cudaGetLastError();
 }
 

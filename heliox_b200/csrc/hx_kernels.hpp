@@ -7,14 +7,26 @@
 
 namespace hx {
 
-size_t fwd_smem_bytes(const DevGroup& G);
-size_t bwd_smem_bytes(const DevGroup& G);
-cudaError_t configure_kernels(size_t smem_fwd, size_t smem_bwd);
+size_t fwd_smem_bytes(const DevGroup& G, int smem_syn = 0);
+size_t bwd_smem_bytes(const DevGroup& G, int smem_syn = 0);
+cudaError_t configure_kernels(size_t smem_fwd, size_t smem_bwd, size_t smem_fwd_net, size_t smem_bwd_net);
 cudaError_t launch_init(const DevGroup& G, const DevState& S, double v_init, cudaStream_t st);
+// N == nullptr: the plain kernels; otherwise the network instantiation
 cudaError_t launch_fwd(const DevGroup& G, const DevState& S, const DevTape& T, int write_tape, const DevProbe& P,
-                       double* trace, const double* tmid, int k0, int k1, cudaStream_t st);
+                       double* trace, const double* tmid, int k0, int k1, cudaStream_t st, const DevNet* N = nullptr);
 cudaError_t launch_bwd(const DevGroup& G, const DevTape& T, const DevAdj& A, const DevGrad& GR, const DevProbe& P,
-                       const double* dLdv, const double* tmid, int k_hi, int k_lo, cudaStream_t st);
+                       const double* dLdv, const double* tmid, int k_hi, int k_lo, cudaStream_t st,
+                       const DevNet* N = nullptr);
+cudaError_t launch_syn_prep(int n, const int* kind, const double* tau1, const double* tau2, double dt, double* cA,
+                            double* cB, double* fA, double* fB, cudaStream_t st);
+cudaError_t launch_init_net(int nsyn, double* sA, double* sB, int ngr, const double* gr_w, const double* gr_vth,
+                            const double* gr_delta, double* gr_g, double* gr_k, double* gr_erev, double* gr_s,
+                            double v_init, cudaStream_t st);
+cudaError_t launch_route(const int2* spk, const int* nspk_dev, int nspk_max, const int* src_off, const int* src_syn,
+                         int nsrc, const double* delay, const double* tstart, int nstep, double half_dt, int k_min,
+                         int* ev_cnt, int* ev_syn, int ev_cap, int* err, cudaStream_t st);
+cudaError_t launch_log_append(const int2* win, const int* win_n, int win_cap, int2* log, int* log_n, int log_cap,
+                              int* err, cudaStream_t st);
 cudaError_t launch_gather(const double* src, const int* idx, double* dst, int n, cudaStream_t st);
 cudaError_t launch_scatter(const double* src, const int* idx, double* dst, int n, cudaStream_t st);
 constexpr int kMsePartials = 256;

@@ -15,121 +15,16 @@
 #include <vector>
 
 #include "heliox_b200.h"
+#include "hx_ctx.hpp"
 #include "hx_dev.hpp"
 #include "hx_kernels.hpp"
 #include "hx_plan.hpp"
 
-namespace {
-
-template <typename T>
-struct DevBuf {
-    T* p = nullptr;
-    size_t n = 0;
-    ~DevBuf() { release(); }
-    void release() {
-        if (p) cudaFree(p);
-        p = nullptr;
-        n = 0;
-    }
-    cudaError_t ensure(size_t count) {
-        if (count <= n && p) return cudaSuccess;
-        release();
-        size_t c = count ? count : 1;
-        cudaError_t e = cudaMalloc((void**)&p, c * sizeof(T));
-        if (e == cudaSuccess) n = c;
-        return e;
-    }
-    cudaError_t upload(const std::vector<T>& v, cudaStream_t st) {
-        cudaError_t e = ensure(v.size());
-        if (e != cudaSuccess || v.empty()) return e;
-        return cudaMemcpyAsync(p, v.data(), v.size() * sizeof(T), cudaMemcpyHostToDevice, st);
-    }
-};
-
-struct PinBuf {
-    void* p = nullptr;
-    size_t bytes = 0;
-    ~PinBuf() {
-        if (p) cudaFreeHost(p);
-    }
-    cudaError_t ensure(size_t b) {
-        if (b <= bytes && p) return cudaSuccess;
-        if (p) cudaFreeHost(p);
-        p = nullptr;
-        bytes = 0;
-        cudaError_t e = cudaMallocHost(&p, b ? b : 16);
-        if (e == cudaSuccess) bytes = b ? b : 16;
-        return e;
-    }
-};
-
-}  // namespace
-
-// Adam over external-gradient slots (one per registered parameter instance).
-struct AdamOpt {
-    double beta1 = 0.9, beta2 = 0.999, eps = 1e-8, impedance = 1.0;
-    long long step = 0;
-    int n = 0;
-    std::vector<int> kind_h, ref_h;
-    DevBuf<int> kind, slot, flat;
-    DevBuf<double> grad, m, v;
-    DevBuf<float> f32;
-};
-
-struct hx_ctx {
-    int device = 0;
-    cudaStream_t own = nullptr, st = nullptr;
-    std::string err;
-    int pack_target = 0;
-    size_t tape_budget = 0;
-    bool loaded = false;
-    hx::Plan P;
-    double dt = 0.025, celsius = 6.3;
-    // plan arrays
-    DevBuf<int> pack_node_off, pack_slot_off, pack_br_off, pack_bch_off, pack_nch_off;
-    DevBuf<int> cs_node0, cs_nnode, cs_warp0, cs_nwarp, cs_bar, cs_lvl_off, cs_nlev, level_br_off;
-    DevBuf<int> br_head, br_end, br_parent, br_child_off, br_child;
-    DevBuf<int> node_parent, node_child_off, node_child, node_flags, node_ic_off, node_ic;
-    // reference instance -> device index, per parameter kind (host + device copies)
-    std::vector<int> kmap_h[HX_P_COUNT];
-    DevBuf<int> kmap[HX_P_COUNT];
-    // parameters: node-indexed (density mechanisms, cm) or per IClamp instance
-    DevBuf<double> a, b, area;
-    DevBuf<double> prm[HX_P_COUNT];
-    DevBuf<double> hh_ena, hh_ek, ic_del, ic_dur;
-    hx::DevGroup G{};
-    // state, tape, checkpoints, adjoint, gradients
-    DevBuf<double> sv, sm, sh, sn;
-    DevBuf<double> tv, tm, th, tn;
-    DevBuf<double> ck;  // nseg x 4 nnode (v, m, h, n)
-    DevBuf<double> lv, lm, lh, ln;
-    DevBuf<double> grad;  // concatenated per kind
-    size_t grad_off[HX_P_COUNT + 1] = {0};
-    DevBuf<double> tmid;
-    int tmid_steps = -1;
-    DevBuf<int> pr_off, pr_local, pr_slot;
-    std::vector<int> probe_key;
-    int nprobe = 0;
-    DevBuf<double> trace_dev, dLdv_dev, stage_dev;
-    DevBuf<double> mse_partial;
-    DevBuf<int> red_off, red_flat;
-    DevBuf<float> red_scale, red_out;
-    PinBuf pin;
-    // capture bookkeeping
-    bool captured = false;
-    int nstep = 0;
-    int seg = 0, nseg = 0;  // steps per segment (checkpoint interval) and count
-    bool full_tape = true;
-    std::vector<AdamOpt*> opts;
-    DevBuf<double*> prm_ptrs;  // device copy of prm[kind].p
-    cudaEvent_t ev[4] = {nullptr, nullptr, nullptr, nullptr};
-    int launches[2] = {0, 0};
-};
-
-static int fail(hx_ctx* c, const std::string& m) {
+int hx_fail(hx_ctx* c, const std::string& m) {
     if (c) c->err = m;
     return -1;
 }
+static int fail(hx_ctx* c, const std::string& m) { return hx_fail(c, m); }
 
 #define HXC(call)                                                                                    \
     do {                                                                                             \
@@ -137,7 +32,8 @@ static int fail(hx_ctx* c, const std::string& m) {
         if (_e != cudaSuccess) return fail(ctx, std::string(#call) + ": " + cudaGetErrorString(_e)); \
     } while (0)
 
-static size_t kind_count(const hx::Plan& P, int kind) {
+static size_t kind_count(const hx_ctx* c, int kind) {
+    const hx::Plan& P = c->P;
     switch (kind) {
         case HX_P_HH_GNABAR:
         case HX_P_HH_GKBAR:
@@ -151,12 +47,52 @@ static size_t kind_count(const hx::Plan& P, int kind) {
             return (size_t)P.nnode;
         case HX_P_IC_AMP:
             return (size_t)P.nic;
+        case HX_P_EXPSYN_W:
+        case HX_P_EXPSYN_E:
+            return (size_t)c->nexp;
+        case HX_P_EXP2SYN_W:
+        case HX_P_EXP2SYN_E:
+            return (size_t)c->nexp2;
+        case HX_P_HALFGAP_G:
+            return (size_t)c->nhg;
+        case HX_P_GAPJ_G:
+        case HX_P_GAPJ_W:
+            return (size_t)c->ngj;
+        case HX_P_GRADED_W:
+            return (size_t)c->ngr;
     }
     return 0;
 }
 
-// device storage length of a kind: node-indexed except IClamp amplitude
-static size_t kind_store(const hx::Plan& P, int kind) { return kind == HX_P_IC_AMP ? (size_t)P.nic : (size_t)P.nnode; }
+// Device storage of a kind: node-indexed for density mechanisms and cm, per
+// instance for IClamp and the network kinds.  ExpSyn and Exp2Syn share one
+// array per variable (GPU synapse order), owned by the ExpSyn kind.
+static size_t kind_store(const hx_ctx* c, int kind) {
+    switch (kind) {
+        case HX_P_IC_AMP:
+            return (size_t)c->P.nic;
+        case HX_P_EXPSYN_W:
+        case HX_P_EXPSYN_E:
+            return (size_t)c->nsyn;
+        case HX_P_EXP2SYN_W:
+        case HX_P_EXP2SYN_E:
+            return 0;
+        case HX_P_HALFGAP_G:
+            return (size_t)c->nhg;
+        case HX_P_GAPJ_G:
+        case HX_P_GAPJ_W:
+            return (size_t)c->ngj;
+        case HX_P_GRADED_W:
+            return (size_t)c->ngr;
+    }
+    return (size_t)c->P.nnode;
+}
+
+static int store_kind(int kind) {
+    return kind == HX_P_EXP2SYN_W ? HX_P_EXPSYN_W : kind == HX_P_EXP2SYN_E ? HX_P_EXPSYN_E : kind;
+}
+double* hx_kind_ptr(hx_ctx* c, int kind) { return c->prm[store_kind(kind)].p; }
+size_t hx_grad_base(const hx_ctx* c, int kind) { return c->grad_off[store_kind(kind)]; }
 
 // dynamic shared memory per CTA of the two step kernels for a plan
 static void plan_smem(const hx::Plan& P, size_t& fwd, size_t& bwd) {
@@ -309,6 +245,7 @@ int hx_load_group(hx_ctx* ctx, const hx_group_desc* desc) {
     ctx->loaded = false;
     ctx->captured = false;
     ctx->probe_key.clear();
+    ctx->tmid_steps = -1;
     // per-CTA node capacity from the opt-in shared memory (backward kernel: 10
     // doubles per node plus the topology tables, about 16 bytes per node)
     int optin = 0;
@@ -349,11 +286,13 @@ int hx_load_group(hx_ctx* ctx, const hx_group_desc* desc) {
         flags[gi] = (P.node_pas[gi] >= 0 ? hx::kHasPas : 0) | (P.node_hh[gi] >= 0 ? hx::kHasHH : 0);
     HXC(ctx->node_flags.upload(flags, st));
 
-    // reference instance -> device slot per kind
-    for (int k = 0; k < HX_P_COUNT; k++) {
+    // network tables (instance orders, kinds 8.. maps, device arrays)
+    if (hx_net_load(ctx, desc)) return -1;
+    // reference instance -> device slot per kind (network kinds: hx_net_load)
+    for (int k = 0; k < HX_P_EXPSYN_W; k++) {
         std::vector<int>& m = ctx->kmap_h[k];
-        m.assign(std::max<size_t>(kind_count(P, k), 1), 0);
-        const size_t cnt = kind_count(P, k);
+        m.assign(std::max<size_t>(kind_count(ctx, k), 1), 0);
+        const size_t cnt = kind_count(ctx, k);
         for (size_t r = 0; r < cnt; r++) {
             if (k <= HX_P_HH_EL)
                 m[r] = P.ref2gpu[desc->hh_node[r]];
@@ -375,8 +314,8 @@ int hx_load_group(hx_ctx* ctx, const hx_group_desc* desc) {
         return out;
     };
     auto inst_arr = [&](int kind, const double* src) {  // density-mechanism instance values -> node slots
-        std::vector<double> out(std::max<size_t>(kind_store(P, kind), 1), 0.0);
-        const size_t cnt = kind_count(P, kind);
+        std::vector<double> out(std::max<size_t>(kind_store(ctx, kind), 1), 0.0);
+        const size_t cnt = kind_count(ctx, kind);
         for (size_t r = 0; r < cnt; r++) out[ctx->kmap_h[kind][r]] = src[r];
         return out;
     };
@@ -405,9 +344,9 @@ int hx_load_group(hx_ctx* ctx, const hx_group_desc* desc) {
     HXC(ctx->lh.ensure(nn));
     HXC(ctx->ln.ensure(nn));
     ctx->grad_off[0] = 0;
-    for (int k = 0; k < HX_P_COUNT; k++) ctx->grad_off[k + 1] = ctx->grad_off[k] + kind_store(P, k);
+    for (int k = 0; k < HX_P_COUNT; k++) ctx->grad_off[k + 1] = ctx->grad_off[k] + kind_store(ctx, k);
     HXC(ctx->grad.ensure(ctx->grad_off[HX_P_COUNT]));
-    HXC(ctx->stage_dev.ensure(ctx->grad_off[HX_P_COUNT] + nn));
+    HXC(ctx->stage_dev.ensure(ctx->grad_off[HX_P_COUNT] + std::max(nn, (size_t)ctx->nsyn)));
 
     hx::DevGroup& G = ctx->G;
     G = hx::DevGroup{};
@@ -462,15 +401,17 @@ int hx_load_group(hx_ctx* ctx, const hx_group_desc* desc) {
     G.cfac = 0.001 * (1.0 / desc->dt);                  // capac.cpp:56,70 with cj = 1/dt
     G.q10 = std::pow(3.0, (desc->celsius - 6.3) / 10);  // hh_templated.cu:90
     size_t sf = hx::fwd_smem_bytes(G), sb = hx::bwd_smem_bytes(G);
+    size_t sfn = hx::fwd_smem_bytes(G, ctx->N.smem_syn), sbn = hx::bwd_smem_bytes(G, ctx->N.smem_syn);
     int maxsmem = 0;
     HXC(cudaDeviceGetAttribute(&maxsmem, cudaDevAttrMaxSharedMemoryPerBlockOptin, ctx->device));
-    if (sb > (size_t)maxsmem || sf > (size_t)maxsmem)
-        return fail(ctx, "cell pack needs " + std::to_string(sb) + " B shared memory (> " + std::to_string(maxsmem) +
+    const size_t need = ctx->net ? sbn : sb;
+    if (need > (size_t)maxsmem || sf > (size_t)maxsmem)
+        return fail(ctx, "cell pack needs " + std::to_string(need) + " B shared memory (> " + std::to_string(maxsmem) +
                              "); lower the pack target or split the cell");
-    HXC(hx::configure_kernels(sf, sb));
+    HXC(hx::configure_kernels(sf, sb, std::min(sfn, (size_t)maxsmem), std::min(sbn, (size_t)maxsmem)));
     {
         std::vector<double*> ptrs(HX_P_COUNT);
-        for (int k = 0; k < HX_P_COUNT; k++) ptrs[k] = ctx->prm[k].p;
+        for (int k = 0; k < HX_P_COUNT; k++) ptrs[k] = hx_kind_ptr(ctx, k);
         HXC(ctx->prm_ptrs.upload(ptrs, st));
     }
     for (AdamOpt* o : ctx->opts) delete o;  // bindings refer to the previous group
@@ -491,7 +432,7 @@ int hx_set_param(hx_ctx* ctx, int kind, const double* values, int n) {
     if (!ctx || !values) return fail(ctx, "null argument");
     if (!ctx->loaded) return fail(ctx, "no group loaded");
     if (kind < 0 || kind >= HX_P_COUNT) return fail(ctx, "bad parameter kind");
-    const size_t cnt = kind_count(ctx->P, kind);
+    const size_t cnt = kind_count(ctx, kind);
     if ((size_t)n != cnt) return fail(ctx, "parameter count mismatch");
     if (!cnt) return 0;
     HXC(cudaSetDevice(ctx->device));
@@ -500,7 +441,7 @@ int hx_set_param(hx_ctx* ctx, int kind, const double* values, int n) {
     memcpy(ctx->pin.p, values, cnt * sizeof(double));
     double* stage = ctx->stage_dev.p;
     HXC(cudaMemcpyAsync(stage, ctx->pin.p, cnt * sizeof(double), cudaMemcpyHostToDevice, ctx->st));
-    HXC(hx::launch_scatter(stage, ctx->kmap[kind].p, ctx->prm[kind].p, (int)cnt, ctx->st));
+    HXC(hx::launch_scatter(stage, ctx->kmap[kind].p, hx_kind_ptr(ctx, kind), (int)cnt, ctx->st));
     HXC(cudaStreamSynchronize(ctx->st));
     return 0;
 }
@@ -509,11 +450,11 @@ int hx_get_param(hx_ctx* ctx, int kind, double* values, int n) {
     if (!ctx || !values) return fail(ctx, "null argument");
     if (!ctx->loaded) return fail(ctx, "no group loaded");
     if (kind < 0 || kind >= HX_P_COUNT) return fail(ctx, "bad parameter kind");
-    const size_t cnt = kind_count(ctx->P, kind);
+    const size_t cnt = kind_count(ctx, kind);
     if ((size_t)n != cnt) return fail(ctx, "parameter count mismatch");
     if (!cnt) return 0;
     HXC(cudaSetDevice(ctx->device));
-    HXC(hx::launch_gather(ctx->prm[kind].p, ctx->kmap[kind].p, ctx->stage_dev.p, (int)cnt, ctx->st));
+    HXC(hx::launch_gather(hx_kind_ptr(ctx, kind), ctx->kmap[kind].p, ctx->stage_dev.p, (int)cnt, ctx->st));
     HXC(cudaMemcpyAsync(values, ctx->stage_dev.p, cnt * sizeof(double), cudaMemcpyDeviceToHost, ctx->st));
     HXC(cudaStreamSynchronize(ctx->st));
     return 0;
@@ -522,7 +463,7 @@ int hx_get_param(hx_ctx* ctx, int kind, double* values, int n) {
 }  // extern "C"
 
 // ---------------------------------------------------------------- capture / backward internals
-static int setup_probes(hx_ctx* ctx, int nprobe, const int* probe_nodes) {
+int hx_setup_probes(hx_ctx* ctx, int nprobe, const int* probe_nodes) {
     if (nprobe < 0 || (nprobe > 0 && !probe_nodes)) return fail(ctx, "bad probe list");
     const hx::Plan& P = ctx->P;
     std::vector<int> key(probe_nodes, probe_nodes + nprobe);
@@ -555,7 +496,7 @@ static int setup_probes(hx_ctx* ctx, int nprobe, const int* probe_nodes) {
     return 0;
 }
 
-static hx::DevProbe probe_view(hx_ctx* c) {
+hx::DevProbe hx_probe_view(hx_ctx* c) {
     hx::DevProbe p;
     p.pack_off = c->pr_off.p;
     p.local = c->pr_local.p;
@@ -564,18 +505,20 @@ static hx::DevProbe probe_view(hx_ctx* c) {
     return p;
 }
 
-static int setup_time(hx_ctx* ctx, int nstep) {
+int hx_setup_time(hx_ctx* ctx, int nstep) {
     // t accumulates in half steps exactly as Simulate::fadvance_cpu does
     // (simulate.cpp:417 and :774); IClamp sees the mid-step value.
     if (ctx->tmid_steps == nstep && ctx->tmid.p) return 0;
-    std::vector<double> tm(std::max(nstep, 1));
+    std::vector<double> tm(std::max(nstep, 1)), ts(std::max(nstep, 1));
     double t = 0.0;
     for (int k = 0; k < nstep; k++) {
+        ts[k] = t;
         t += 0.5 * ctx->dt;
         tm[k] = t;
         t += 0.5 * ctx->dt;
     }
     HXC(ctx->tmid.upload(tm, ctx->st));
+    HXC(ctx->tstart.upload(ts, ctx->st));
     HXC(cudaStreamSynchronize(ctx->st));  // the source vector is pageable and goes out of scope
     ctx->tmid_steps = nstep;
     return 0;
@@ -638,15 +581,16 @@ static int run_forward(hx_ctx* ctx, int nstep, double v_init, int nprobe, const 
     if (!ctx->loaded) return fail(ctx, "no group loaded");
     if (nstep < 0) return fail(ctx, "nstep must be >= 0");
     HXC(cudaSetDevice(ctx->device));
-    if (setup_probes(ctx, nprobe, probe)) return -1;
-    if (setup_time(ctx, nstep)) return -1;
+    if (hx_setup_probes(ctx, nprobe, probe)) return -1;
+    if (hx_setup_time(ctx, nstep)) return -1;
+    if (ctx->net) return hx_net_forward(ctx, nstep, v_init, trace_dev, capture);
     hx::DevTape T{nullptr, nullptr, nullptr, nullptr, 0};
     if (capture) {
         if (plan_tape(ctx, nstep)) return -1;
         T = hx::DevTape{ctx->tv.p, ctx->tm.p, ctx->th.p, ctx->tn.p, 0};
     }
     hx::DevState S = state_view(ctx);
-    hx::DevProbe PV = probe_view(ctx);
+    hx::DevProbe PV = hx_probe_view(ctx);
     HXC(hx::launch_init(ctx->G, S, v_init, ctx->st));
     HXC(cudaEventRecord(ctx->ev[0], ctx->st));
     int launches = 0;
@@ -672,6 +616,7 @@ static int run_backward(hx_ctx* ctx, const double* dLdv_dev) {
     if (!ctx->loaded) return fail(ctx, "no group loaded");
     if (!ctx->captured) return fail(ctx, "hx_backward needs a preceding hx_forward_capture");
     HXC(cudaSetDevice(ctx->device));
+    if (ctx->net) return hx_net_backward(ctx, dLdv_dev);
     const size_t nn = ctx->P.nnode;
     HXC(cudaMemsetAsync(ctx->lv.p, 0, nn * 8, ctx->st));
     HXC(cudaMemsetAsync(ctx->lm.p, 0, nn * 8, ctx->st));
@@ -683,7 +628,7 @@ static int run_backward(hx_ctx* ctx, const double* dLdv_dev) {
     hx::DevGrad GR{g + ctx->grad_off[HX_P_HH_GNABAR], g + ctx->grad_off[HX_P_HH_GKBAR], g + ctx->grad_off[HX_P_HH_GL],
                    g + ctx->grad_off[HX_P_HH_EL],     g + ctx->grad_off[HX_P_PAS_G],   g + ctx->grad_off[HX_P_PAS_E],
                    g + ctx->grad_off[HX_P_CM],        g + ctx->grad_off[HX_P_IC_AMP]};
-    hx::DevProbe PV = probe_view(ctx);
+    hx::DevProbe PV = hx_probe_view(ctx);
     hx::DevState S = state_view(ctx);
     HXC(cudaEventRecord(ctx->ev[2], ctx->st));
     int launches = 0;
@@ -711,8 +656,8 @@ static int gather_grads_dev(hx_ctx* ctx, double* const* grads_dev) {
     if (!grads_dev) return 0;
     for (int k = 0; k < HX_P_COUNT; k++) {
         if (!grads_dev[k]) continue;
-        const size_t cnt = kind_count(ctx->P, k);
-        HXC(hx::launch_gather(ctx->grad.p + ctx->grad_off[k], ctx->kmap[k].p, grads_dev[k], (int)cnt, ctx->st));
+        const size_t cnt = kind_count(ctx, k);
+        HXC(hx::launch_gather(ctx->grad.p + hx_grad_base(ctx, k), ctx->kmap[k].p, grads_dev[k], (int)cnt, ctx->st));
     }
     return 0;
 }
@@ -755,10 +700,10 @@ int hx_backward(hx_ctx* ctx, const double* dLdv, double* const* grads) {
     if (grads) {
         for (int k = 0; k < HX_P_COUNT; k++) {
             if (!grads[k]) continue;
-            const size_t cnt = kind_count(ctx->P, k);
+            const size_t cnt = kind_count(ctx, k);
             if (!cnt) continue;
             double* sd = ctx->stage_dev.p + ctx->grad_off[k];
-            HXC(hx::launch_gather(ctx->grad.p + ctx->grad_off[k], ctx->kmap[k].p, sd, (int)cnt, ctx->st));
+            HXC(hx::launch_gather(ctx->grad.p + hx_grad_base(ctx, k), ctx->kmap[k].p, sd, (int)cnt, ctx->st));
             HXC(cudaMemcpyAsync(grads[k], sd, cnt * 8, cudaMemcpyDeviceToHost, ctx->st));
         }
     }
@@ -782,7 +727,7 @@ int hx_reduce_grads_f32(hx_ctx* ctx, int n, const int* kind, const int* index, c
     for (int e = 0; e < n; e++) {
         if (dest[e] < 0 || dest[e] >= n_out) return fail(ctx, "dest out of range");
         if (kind[e] < 0 || kind[e] >= HX_P_COUNT) return fail(ctx, "bad kind");
-        if (index[e] < 0 || (size_t)index[e] >= kind_count(ctx->P, kind[e])) return fail(ctx, "index out of range");
+        if (index[e] < 0 || (size_t)index[e] >= kind_count(ctx, kind[e])) return fail(ctx, "index out of range");
         cnt[dest[e] + 1]++;
     }
     for (int c = 0; c < n_out; c++) cnt[c + 1] += cnt[c];
@@ -792,7 +737,7 @@ int hx_reduce_grads_f32(hx_ctx* ctx, int n, const int* kind, const int* index, c
     std::vector<float> sc(std::max(n, 1));
     for (int e = 0; e < n; e++) {
         const int pos = fill[dest[e]]++;
-        flat[pos] = (int)ctx->grad_off[kind[e]] + ctx->kmap_h[kind[e]][index[e]];
+        flat[pos] = (int)hx_grad_base(ctx, kind[e]) + ctx->kmap_h[kind[e]][index[e]];
         sc[pos] = scale[e];
     }
     HXC(ctx->red_off.upload(cnt, ctx->st));
@@ -857,10 +802,10 @@ int hx_opt_add_params(hx_ctx* ctx, int opt, int n, const int* kind, const int* i
     std::vector<int> kv(n), sv(n), fv(n);
     for (int i = 0; i < n; i++) {
         if (kind[i] < 0 || kind[i] >= HX_P_COUNT) return fail(ctx, "bad parameter kind");
-        if (index[i] < 0 || (size_t)index[i] >= kind_count(ctx->P, kind[i])) return fail(ctx, "parameter index out of range");
+        if (index[i] < 0 || (size_t)index[i] >= kind_count(ctx, kind[i])) return fail(ctx, "parameter index out of range");
         kv[i] = kind[i];
         sv[i] = ctx->kmap_h[kind[i]][index[i]];
-        fv[i] = (int)ctx->grad_off[kind[i]] + sv[i];
+        fv[i] = (int)hx_grad_base(ctx, kind[i]) + sv[i];
     }
     o->kind_h = kv;
     o->ref_h.assign(index, index + n);

@@ -28,6 +28,14 @@ _MECH_VAR = {
     ("pas", "e"): "pas.e",
     ("capacitance", "cm"): "cm",
     ("IClamp", "amp"): "IClamp.amp",
+    ("ExpSyn", "weight"): "ExpSyn.weight",
+    ("ExpSyn", "e"): "ExpSyn.e",
+    ("Exp2Syn", "weight"): "Exp2Syn.weight",
+    ("Exp2Syn", "e"): "Exp2Syn.e",
+    ("HalfGap", "g"): "HalfGap.g",
+    ("gapjunction_lr", "g"): "gapjunction_lr.g",
+    ("gapjunction_lr", "w"): "gapjunction_lr.w",
+    ("neuron_to_neuron_syn_lr", "w"): "neuron_to_neuron_syn_lr.w",
 }
 _HANDLE_SHIFT = 24
 
@@ -84,10 +92,13 @@ class Sim:
         """Launch on an existing CUDA stream (e.g. ``torch.cuda.current_stream().cuda_stream``)."""
         self._check(self._L.hx_set_stream(self._ctx, C.c_void_p(int(stream_handle))), "hx_set_stream")
 
-    def load_group(self, group: CellGroup):
+    def load_group(self, group: CellGroup, gid_base: int = 0, nsrc_cells: int = 0):
+        """Load a cell group.  For one shard of a multi-GPU network, ``gid_base``
+        is the global id of its first cell and ``nsrc_cells`` the number of cells
+        over all shards (NetCon sources and NetStims then use global ids)."""
         group.validate()
         self.group = group
-        self._bound = _lib.BoundGroup(group)
+        self._bound = _lib.BoundGroup(group, gid_base=gid_base, nsrc_cells=nsrc_cells)
         self._check(self._L.hx_load_group(self._ctx, C.byref(self._bound.desc)), "hx_load_group")
 
     def plan_stats(self) -> dict:
@@ -108,13 +119,54 @@ class Sim:
 
     def _count(self, key: str) -> int:
         g = self.group
-        if key.startswith("hh."):
-            return g.hh.n
-        if key.startswith("pas."):
-            return g.pas.n
+        mech = key.split(".")[0]
+        tab = {"hh": g.hh, "pas": g.pas, "IClamp": g.iclamp, "ExpSyn": g.expsyn, "Exp2Syn": g.exp2syn,
+               "HalfGap": g.halfgap, "gapjunction_lr": g.gapjunction, "neuron_to_neuron_syn_lr": g.graded}.get(mech)
         if key == "cm":
             return g.nnode
-        return g.iclamp.n
+        return tab.n
+
+    # ------------------------------------------------------------------ network
+    def spikes(self):
+        """Spikes of the group's PreSyns in the last forward: (gid int32[n], t float64[n]),
+        in detection order (the reference's spk.dat holds the same pairs)."""
+        n = C.c_int(0)
+        self._check(self._L.hx_get_spikes(self._ctx, 0, _lib._ip(), _lib._dp(), C.byref(n)), "hx_get_spikes")
+        k = int(n.value)
+        gid = np.zeros(max(k, 1), dtype=np.int32)
+        t = np.zeros(max(k, 1))
+        self._check(self._L.hx_get_spikes(self._ctx, k, _lib.iptr(gid), _lib.dptr(t), C.byref(n)), "hx_get_spikes")
+        return gid[:k], t[:k]
+
+    def set_exchange(self, fn, nranks: int):
+        """Install the multi-GPU spike exchange: ``fn(send_ptr, recv_ptr, cap_entries, stream_ptr)``
+        must all-gather ``cap_entries`` int pairs per rank from ``send_ptr`` into
+        ``recv_ptr`` on the given stream (``None`` removes it)."""
+        if fn is None:
+            self._xfn = None
+            self._check(self._L.hx_set_exchange(self._ctx, _lib.EXCHANGE_FN(), None, 1), "hx_set_exchange")
+            return
+
+        def cb(user, send, recv, cap, stream):
+            try:
+                fn(int(send or 0), int(recv or 0), int(cap), int(stream or 0))
+                return 0
+            except Exception:  # an exception must not cross the C boundary
+                import traceback
+
+                traceback.print_exc()
+                return -1
+
+        self._xfn = _lib.EXCHANGE_FN(cb)
+        self._check(self._L.hx_set_exchange(self._ctx, self._xfn, None, int(nranks)), "hx_set_exchange")
+
+    def set_window(self, steps: int):
+        self._check(self._L.hx_set_window(self._ctx, int(steps)), "hx_set_window")
+
+    def window(self) -> int:
+        w = C.c_int(0)
+        self._check(self._L.hx_get_window(self._ctx, C.byref(w)), "hx_get_window")
+        return int(w.value)
 
     def set_param_array(self, key: str, values: np.ndarray):
         v = np.ascontiguousarray(values, dtype=np.float64)

@@ -20,7 +20,7 @@
 extern "C" {
 #endif
 
-#define HX_ABI_VERSION 1
+#define HX_ABI_VERSION 2
 
 typedef struct hx_ctx hx_ctx;
 
@@ -46,6 +46,41 @@ typedef struct hx_group_desc {
     int nic;
     const int* ic_node;
     const double *ic_del, *ic_dur, *ic_amp;
+
+    /* ---- network (all counts may be 0; the pointers are then ignored) ----
+     * Spike sources are global ids: gid_base + local cell (this group's
+     * cells' PreSyns, threshold detection at the cell's root node,
+     * src/spike/presyn.cpp:133-177), 0..nsrc_cells-1 over all groups of a
+     * multi-GPU job, then nsrc_cells + j for NetStim j.  Every ExpSyn /
+     * Exp2Syn instance is the target of exactly one NetCon (src, delay ms,
+     * weight uS): the per-instance spk_vec_idx / delay / weights the
+     * reference fills in initSynapse (src/io/coredat_to_innerdat.cpp:348-376). */
+    int gid_base, nsrc_cells;       /* 0, 0 = this group alone (nsrc_cells = ncell) */
+    const double* ps_thresh;        /* ncell thresholds (mV); NULL = 10 mV */
+    /* ExpSyn (src/spike/postsyn_mech/expsyn.cpp) */
+    int nexpsyn;
+    const int *expsyn_node, *expsyn_src;
+    const double *expsyn_tau, *expsyn_e, *expsyn_delay, *expsyn_weight;
+    /* Exp2Syn (src/spike/user_postsyn_mech/exp2syn_temp.cuh) */
+    int nexp2syn;
+    const int *exp2syn_node, *exp2syn_src;
+    const double *exp2syn_tau1, *exp2syn_tau2, *exp2syn_e, *exp2syn_delay, *exp2syn_weight;
+    /* NetStim (src/spike/netstim.cpp): the same table on every rank */
+    int nnetstim;
+    const double *ns_interval, *ns_number, *ns_start, *ns_noise;
+    int netstim_rng; /* 0: the reference's CPU-mode stream (zeroed state), 1: GPU mode (sequence 0) */
+    /* HalfGap (src/mech/user-mech/HalfGap.cu): vgap follows v of node hg_src */
+    int nhalfgap;
+    const int *hg_node, *hg_src;
+    const double* hg_g;
+    /* gapjunction_lr (src/mech/worm-lr-mech/gapjunction_lr.cu): vpre = v of node gj_pre */
+    int ngapj;
+    const int *gj_node, *gj_pre;
+    const double *gj_g, *gj_w;
+    /* neuron_to_neuron_syn_lr (src/mech/worm-lr-mech/neuron_to_neuron_syn_lr.cu) */
+    int ngraded;
+    const int *gr_node, *gr_pre;
+    const double *gr_w, *gr_delta, *gr_vth;
 } hx_group_desc;
 
 /* Parameter / gradient kinds (per mechanism instance; HX_P_CM per node). */
@@ -58,7 +93,15 @@ enum hx_param_kind {
     HX_P_PAS_E = 5,
     HX_P_CM = 6,
     HX_P_IC_AMP = 7,
-    HX_P_COUNT = 8
+    HX_P_EXPSYN_W = 8,    /* NetCon weight into ExpSyn instance i */
+    HX_P_EXPSYN_E = 9,
+    HX_P_EXP2SYN_W = 10,  /* NetCon weight into Exp2Syn instance i */
+    HX_P_EXP2SYN_E = 11,
+    HX_P_HALFGAP_G = 12,
+    HX_P_GAPJ_G = 13,
+    HX_P_GAPJ_W = 14,
+    HX_P_GRADED_W = 15,
+    HX_P_COUNT = 16
 };
 
 /* Statistics of the execution plan built at load time. */
@@ -123,6 +166,37 @@ int hx_simulate(hx_ctx* ctx, int nstep, double v_init, int nprobe, const int* pr
 int hx_forward_capture(hx_ctx* ctx, int nstep, double v_init, int nprobe, const int* probe_nodes, double* trace);
 int hx_forward_capture_dev(hx_ctx* ctx, int nstep, double v_init, int nprobe, const int* probe_nodes,
                            double* trace_dev);
+
+/* ---- network ------------------------------------------------------------------ */
+/* Spikes of this group's PreSyns detected by the last forward, in detection
+ * order: global source gid and time (ms).  *n receives the total count (which
+ * may exceed cap).  Replaces Simulate::output_spikes / rec_spikes
+ * (src/simulate.cpp:881-899). */
+int hx_get_spikes(hx_ctx* ctx, int cap, int* gid, double* t, int* n);
+/* Multi-GPU spike exchange.  A group whose NetCons name sources of other
+ * groups (nsrc_cells > ncell) advances in windows no longer than the smallest
+ * NetCon delay; after every window the library calls
+ *   exchange(user, send_dev, recv_dev, cap_entries, stream)
+ * where send_dev holds this group's window spikes as cap_entries int pairs
+ * (global source gid, step) padded with (-1, -1), and recv_dev (nranks x
+ * cap_entries pairs) must receive every rank's send buffer (an all-gather on
+ * `stream`, e.g. ncclAllGather) before the callback returns.  All ranks must
+ * use the same window (hx_set_window) and call the forward together.  The
+ * reference exchanges through its host spike queue
+ * (Simulate::network_spike_send_cpu / network_spike_receive_cpu,
+ * src/simulate.cpp:858-951). */
+/* NetStim spike trains of a group over finitialize + nstep steps, computed on
+ * the host (no device needed): NetStim instance and the step at whose start
+ * it fires (0 for the delivery at finitialize), in emission order.  *n gets
+ * the total count (may exceed cap).  These are the artificial-cell events of
+ * the reference's NetStim (src/spike/netstim.cpp:207-330). */
+int hx_netstim_trains(const hx_group_desc* desc, int nstep, int cap, int* id, int* step, int* n);
+typedef int (*hx_exchange_fn)(void* user, const void* send_dev, void* recv_dev, int cap_entries, void* stream);
+int hx_set_exchange(hx_ctx* ctx, hx_exchange_fn exchange, void* user, int nranks);
+/* Steps per forward window of an event network (0 = derived from the smallest
+ * NetCon delay of this group); returns the effective value with hx_get_window. */
+int hx_set_window(hx_ctx* ctx, int steps);
+int hx_get_window(hx_ctx* ctx, int* steps);
 
 /* ---- backward ------------------------------------------------------------------ */
 /* Exact discrete adjoint of the captured forward.  dLdv: (nstep+1) x nprobe,

@@ -430,6 +430,14 @@ static int ns_receive(const hxo_group* g, hxo_state* s, double t, double tt) {
             /* net_send NORMAL_EVENT: the NetStim's slot in the spike vector */
             s->spk_flag[g->ncell + i] = SPK_NORMAL;
             s->spk_t[g->ncell + i] = t;
+            {
+                hxo_net* Nm = g->net;
+                if (Nm->ns_nspike < Nm->ns_spike_cap) {
+                    Nm->ns_spike_id[Nm->ns_nspike] = i;
+                    Nm->ns_spike_t[Nm->ns_nspike] = t;
+                }
+                Nm->ns_nspike++;
+            }
             ns_next_invl(N, s);
             if (s->ns_on[i] == 1.0) {
                 ns_push(s, t + s->ns_event[i], i, SPK_SELF);
@@ -741,7 +749,7 @@ static void record(const hxo_group* g, const hxo_state* s, int nprobe, const int
 int hxo_forward(const hxo_group* g, double v_init, int nstep, int nprobe, const int* probe, double* trace,
                 double* v_final, double* m_final, double* h_final, double* n_final) {
     hxo_state s;
-    if (g->net) g->net->nspike = 0;
+    if (g->net) g->net->nspike = g->net->ns_nspike = 0;
     if (state_alloc(g, &s)) {
         state_free(&s);
         return -1;
@@ -802,7 +810,7 @@ int hxo_adjoint(const hxo_group* g, double v_init, int nstep, int nprobe, const 
     if (!tv || !tm || !th || !tn || !tA || !tB || !tS || !tmid || !ev_off || !lv || !mu || !w || !dd || !lm || !lh ||
         !ln || !lA || !lB || !lS)
         goto done;
-    if (N) N->nspike = 0;
+    if (N) N->nspike = N->ns_nspike = 0;
     if (state_alloc(g, &s)) goto done;
 
     /* ---- forward with a full tape: state at the start of every step, the

@@ -49,6 +49,11 @@ typedef struct hxo_net {
     int* spike_gid;
     double* spike_t;
     int nspike; /* total detected (may exceed spike_cap) */
+    /* NetStim spikes (instance, time) in emission order */
+    int ns_spike_cap;
+    int* ns_spike_id;
+    double* ns_spike_t;
+    int ns_nspike;
 } hxo_net;
 
 typedef struct hxo_group {

@@ -34,6 +34,7 @@ class _Net(C.Structure):
         ("ngr", C.c_int), ("gr_node", _ip), ("gr_pre", _ip), ("gr_w", _dp), ("gr_g", _dp), ("gr_delta", _dp),
         ("gr_k", _dp), ("gr_vth", _dp), ("gr_erev", _dp),
         ("spike_cap", C.c_int), ("spike_gid", _ip), ("spike_t", _dp), ("nspike", C.c_int),
+        ("ns_spike_cap", C.c_int), ("ns_spike_id", _ip), ("ns_spike_t", _dp), ("ns_nspike", C.c_int),
     ]
 
 
@@ -268,9 +269,19 @@ class _Bound:
             self.spk_gid = np.zeros(cap, dtype=np.int32)
             self.spk_t = np.zeros(cap)
             n.spike_cap, n.spike_gid, n.spike_t, n.nspike = cap, _i(self.spk_gid), _d(self.spk_t), 0
+            self.ns_id = np.zeros(cap, dtype=np.int32)
+            self.ns_t = np.zeros(cap)
+            n.ns_spike_cap, n.ns_spike_id, n.ns_spike_t, n.ns_nspike = cap, _i(self.ns_id), _d(self.ns_t), 0
             self.net = n
             s.net = C.pointer(n)
         self.s = s
+
+    def netstim_spikes(self):
+        """NetStim spikes as a list of (t, instance) in emission order."""
+        if self.net is None:
+            return []
+        k = min(self.net.ns_nspike, self.net.ns_spike_cap)
+        return [(float(self.ns_t[i]), int(self.ns_id[i])) for i in range(k)]
 
     def spikes(self):
         """Detected PreSyn spikes as a list of (t, gid) in detection order."""
@@ -293,7 +304,8 @@ def forward(g, nstep: int, probe: Optional[Sequence[int]] = None, v_init: Option
                        _i(probe), _d(trace), _d(vf), _d(mf), _d(hf), _d(nf))
     if rc != 0:
         raise RuntimeError("oracle forward failed")
-    return trace, {"v": vf, "m": mf[: g.hh.n], "h": hf[: g.hh.n], "n": nf[: g.hh.n], "spikes": b.spikes()}
+    return trace, {"v": vf, "m": mf[: g.hh.n], "h": hf[: g.hh.n], "n": nf[: g.hh.n], "spikes": b.spikes(),
+                   "netstim_spikes": b.netstim_spikes()}
 
 
 GRAD_KEYS = ("hh.gnabar", "hh.gkbar", "hh.gl", "hh.el", "pas.g", "pas.e", "cm", "IClamp.amp")
