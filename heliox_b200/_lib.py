@@ -137,7 +137,7 @@ SIGNATURES = {
     "hx_opt_reset": (C.c_int, [C.c_void_p, C.c_int]),
     "hx_get_spikes": (C.c_int, [C.c_void_p, C.c_int, _ip, _dp, _ip]),
     "hx_netstim_trains": (C.c_int, [C.POINTER(GroupDesc), C.c_int, C.c_int, _ip, _ip, _ip]),
-    "hx_set_exchange": (C.c_int, [C.c_void_p, EXCHANGE_FN, C.c_void_p, C.c_int]),
+    "hx_set_exchange": (C.c_int, [C.c_void_p, EXCHANGE_FN, C.c_void_p, C.c_int, C.c_int]),
     "hx_set_window": (C.c_int, [C.c_void_p, C.c_int]),
     "hx_get_window": (C.c_int, [C.c_void_p, _ip]),
 }

@@ -143,7 +143,7 @@ struct hx_ctx {
     int ev_cap = 0;
     DevBuf<int2> win_send, win_recv, spk_log, ns_spk;
     DevBuf<int> win_n, log_n;
-    int win_cap = 0, log_cap = 0;
+    int win_cap = 0, log_cap = 0, win_cap_user = 0;
     // NetStim trains of the last forward length (host generator, routed each forward)
     std::vector<double> ns_interval, ns_number, ns_start, ns_noise;
     int ns_rng = 0, ns_steps = -1, ns_count = 0;

@@ -412,6 +412,11 @@ int hx_net_forward(hx_ctx* ctx, int nstep, double v_init, double* trace_dev, boo
     if (capture && net_plan_tape(ctx, nstep, W)) return -1;
     const int ncell = (int)P.cs_node0.size();
     ctx->win_cap = ncell * ((W + 1) / 2) + 1;
+    if (ctx->win_cap_user > 0) {  // all ranks must exchange buffers of one size
+        if (ctx->win_cap_user < ctx->win_cap)
+            return hx_fail(ctx, "exchange capacity below this group's bound of " + std::to_string(ctx->win_cap));
+        ctx->win_cap = ctx->win_cap_user;
+    }
     HXC(ctx->win_send.ensure(ctx->win_cap));
     HXC(ctx->win_recv.ensure((size_t)ctx->win_cap * std::max(ctx->nranks, 1)));
     ctx->log_cap = (int)std::min<long long>((long long)ncell * std::max(64, nstep / 20 + 1), 1LL << 26);
@@ -655,12 +660,13 @@ int hx_netstim_trains(const hx_group_desc* d, int nstep, int cap, int* id, int* 
     return 0;
 }
 
-int hx_set_exchange(hx_ctx* ctx, hx_exchange_fn exchange, void* user, int nranks) {
+int hx_set_exchange(hx_ctx* ctx, hx_exchange_fn exchange, void* user, int nranks, int cap_entries) {
     if (!ctx) return -1;
-    if (nranks < 1) return hx_fail(ctx, "nranks must be >= 1");
+    if (nranks < 1 || cap_entries < 0) return hx_fail(ctx, "nranks must be >= 1, cap_entries >= 0");
     ctx->exchange = exchange;
     ctx->exchange_user = user;
     ctx->nranks = exchange ? nranks : 1;
+    ctx->win_cap_user = exchange ? cap_entries : 0;
     ctx->ev_cap = 0;
     return 0;
 }

@@ -189,7 +189,8 @@ class CellGroup:
             for k, v in tab.fields.items():
                 if v.shape != (tab.n,) or v.dtype != F64:
                     raise ValueError(f"{nm}.{k} must be float64[{tab.n}]")
-        nsrc = self.ncell + self.netstim.n
+        # a shard of a multi-GPU network keeps global NetCon sources
+        nsrc = int(self.meta.get("nsrc_cells", self.ncell)) + self.netstim.n
         for tab, nm, fl in ((self.expsyn, "ExpSyn", EXPSYN_FIELDS), (self.exp2syn, "Exp2Syn", EXP2SYN_FIELDS),
                             (self.halfgap, "HalfGap", HALFGAP_FIELDS), (self.gapjunction, "gapjunction_lr",
                                                                         GAPJ_FIELDS),

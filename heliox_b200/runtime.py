@@ -138,13 +138,14 @@ class Sim:
         self._check(self._L.hx_get_spikes(self._ctx, k, _lib.iptr(gid), _lib.dptr(t), C.byref(n)), "hx_get_spikes")
         return gid[:k], t[:k]
 
-    def set_exchange(self, fn, nranks: int):
+    def set_exchange(self, fn, nranks: int, cap_entries: int = 0):
         """Install the multi-GPU spike exchange: ``fn(send_ptr, recv_ptr, cap_entries, stream_ptr)``
-        must all-gather ``cap_entries`` int pairs per rank from ``send_ptr`` into
-        ``recv_ptr`` on the given stream (``None`` removes it)."""
+        must all-gather ``cap_entries`` (gid, step) int pairs per rank from
+        ``send_ptr`` into ``recv_ptr`` on the given stream (``None`` removes it).
+        ``cap_entries`` must be the same on every rank (``shard.exchange_capacity``)."""
         if fn is None:
             self._xfn = None
-            self._check(self._L.hx_set_exchange(self._ctx, _lib.EXCHANGE_FN(), None, 1), "hx_set_exchange")
+            self._check(self._L.hx_set_exchange(self._ctx, _lib.EXCHANGE_FN(), None, 1, 0), "hx_set_exchange")
             return
 
         def cb(user, send, recv, cap, stream):
@@ -158,7 +159,8 @@ class Sim:
                 return -1
 
         self._xfn = _lib.EXCHANGE_FN(cb)
-        self._check(self._L.hx_set_exchange(self._ctx, self._xfn, None, int(nranks)), "hx_set_exchange")
+        self._check(self._L.hx_set_exchange(self._ctx, self._xfn, None, int(nranks), int(cap_entries)),
+                    "hx_set_exchange")
 
     def set_window(self, steps: int):
         self._check(self._L.hx_set_window(self._ctx, int(steps)), "hx_set_window")

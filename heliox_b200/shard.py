@@ -46,7 +46,8 @@ def shard(g: CellGroup, nranks: int, rank: int) -> Tuple[CellGroup, int, int]:
     Returns (group, gid_base, nsrc_cells): the shard's cells in the original
     order (roots first), its synapses with global NetCon sources, the whole
     NetStim table; ``gid_base`` is the global id of its first cell and
-    ``nsrc_cells`` the number of cells over all shards.
+    ``nsrc_cells`` the number of cells over all shards.  The group's
+    ``meta["global_index"]`` maps its synapse instances to the network's.
     """
     if g.coupled:
         raise ValueError("gap junctions and graded synapses are not partitioned across ranks")
@@ -61,10 +62,14 @@ def shard(g: CellGroup, nranks: int, rank: int) -> Tuple[CellGroup, int, int]:
     par = g.parent[order].astype(np.int64)
     parent = np.where(par >= 0, new[np.maximum(par, 0)], -1)
 
-    def sub(tab: MechTable) -> MechTable:
+    global_index = {}
+
+    def sub(tab: MechTable, name: str = "") -> MechTable:
         m = np.isin(tab.nodes, keep)
         nodes = new[tab.nodes[m]]
         o = np.argsort(nodes, kind="stable")
+        if name:
+            global_index[name] = np.nonzero(m)[0][o]
         return MechTable(_i32(nodes[o]), {k: _f64(v[m][o]) for k, v in tab.fields.items()},
                          {k: _i32(v[m][o]) for k, v in tab.ifields.items()})
 
@@ -82,12 +87,17 @@ def shard(g: CellGroup, nranks: int, rank: int) -> Tuple[CellGroup, int, int]:
         dt=g.dt,
         v_init=g.v_init,
         name=f"{g.name}.rank{rank}of{nranks}",
-        expsyn=sub(g.expsyn),
-        exp2syn=sub(g.exp2syn),
+        expsyn=sub(g.expsyn, "ExpSyn"),
+        exp2syn=sub(g.exp2syn, "Exp2Syn"),
         netstim=g.netstim.copy(),
         ps_thresh=_f64(g.ps_thresh[c0:c1]),
         netstim_rng=g.netstim_rng,
     )
+    # instance i of the shard's ExpSyn / Exp2Syn table is global instance
+    # meta["global_index"][mech][i]
+    out.meta["global_index"] = global_index
+    out.meta["nsrc_cells"] = g.ncell
+    out.meta["gid_base"] = c0
     # NetCon sources stay global: validate against the global source count
     nsrc = g.ncell + g.netstim.n
     for tab in (out.expsyn, out.exp2syn):
@@ -105,6 +115,13 @@ def window_of(g: CellGroup) -> int:
         return 1 << 30
     lag = np.floor((d.min() - 0.5 * g.dt) / g.dt) - 1.0
     return int(max(1.0, lag))
+
+
+def exchange_capacity(g: CellGroup, nranks: int, window: int) -> int:
+    """Window spike buffer size shared by all ranks: the largest shard's cells
+    times ceil(window/2) (a PreSyn fires at most every other step) plus one."""
+    most = max(c1 - c0 for c0, c1 in cell_ranges(g, nranks))
+    return most * ((window + 1) // 2) + 1
 
 
 def allgather_exchange(group=None):

@@ -192,7 +192,10 @@ int hx_get_spikes(hx_ctx* ctx, int cap, int* gid, double* t, int* n);
  * the reference's NetStim (src/spike/netstim.cpp:207-330). */
 int hx_netstim_trains(const hx_group_desc* desc, int nstep, int cap, int* id, int* step, int* n);
 typedef int (*hx_exchange_fn)(void* user, const void* send_dev, void* recv_dev, int cap_entries, void* stream);
-int hx_set_exchange(hx_ctx* ctx, hx_exchange_fn exchange, void* user, int nranks);
+/* cap_entries: the window buffer size, identical on every rank and at least
+ * (this group's cells) * ceil(window / 2) (a PreSyn fires at most every other
+ * step); pass the maximum over ranks.  0 = this group's own bound (one rank). */
+int hx_set_exchange(hx_ctx* ctx, hx_exchange_fn exchange, void* user, int nranks, int cap_entries);
 /* Steps per forward window of an event network (0 = derived from the smallest
  * NetCon delay of this group); returns the effective value with hx_get_window. */
 int hx_set_window(hx_ctx* ctx, int steps);
