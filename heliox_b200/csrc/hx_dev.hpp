@@ -5,7 +5,7 @@
 
 namespace hx {
 
-constexpr int kThreads = 256;  // threads per CTA (one CTA per cell pack, 8 warps)
+constexpr int kThreads = 512;  // threads per CTA (one CTA per cell pack, 16 warps, one CTA per SM)
 
 enum NodeFlag : int { kHasPas = 1, kHasHH = 2 };
 

@@ -395,7 +395,7 @@ __global__ void init_state_kernel(DevGroup G, DevState S, double v_init) {
 // synapses; one step) partner voltages come from N.vpeer and v_{k+1} goes to
 // N.vout, so that no CTA reads a value another CTA rewrites.
 template <bool kNet>
-__global__ void __launch_bounds__(kThreads, 2) fwd_kernel(DevGroup G, DevState S, DevTape T, int write_tape,
+__global__ void __launch_bounds__(kThreads, 1) fwd_kernel(DevGroup G, DevState S, DevTape T, int write_tape,
                                                            DevProbe P, double* __restrict__ trace,
                                                            const double* __restrict__ tmid, int k0, int k1, DevNet N) {
     extern __shared__ double smem[];
@@ -585,7 +585,7 @@ __global__ void __launch_bounds__(kThreads, 2) fwd_kernel(DevGroup G, DevState S
 // synapse to its partner node go through N.x_*_out and are gathered by the
 // launch of step k-1 from N.x_*_in, in the fixed order of N.node_in.
 template <bool kNet>
-__global__ void __launch_bounds__(kThreads, 2) bwd_kernel(DevGroup G, DevTape T, DevAdj Ad, DevGrad GR, DevProbe P,
+__global__ void __launch_bounds__(kThreads, 1) bwd_kernel(DevGroup G, DevTape T, DevAdj Ad, DevGrad GR, DevProbe P,
                                                            const double* __restrict__ dLdv,
                                                            const double* __restrict__ tmid, int k_hi, int k_lo,
                                                            DevNet N) {

@@ -117,8 +117,11 @@ std::string build_plan(const hx_group_desc& g, int nodes_per_warp, int max_pack_
         });
     }
 
-    // warps per cell and first-fit-decreasing packing into CTAs of kWarpsPerCta
-    // warps with a node capacity (shared memory)
+    // first-fit-decreasing packing of whole cells into CTAs by node count (the
+    // shared-memory capacity; at most kWarpsPerCta cells), then the CTA's warps
+    // are shared among its cells in proportion to their nodes (at least one
+    // each, largest remainders first), so every thread of a CTA carries about
+    // the same number of nodes.
     const int npw = nodes_per_warp > 0 ? nodes_per_warp : 144;
     const int maxcell = *std::max_element(cell_size.begin(), cell_size.end());
     int cap = npw * kWarpsPerCta;
@@ -129,46 +132,61 @@ std::string build_plan(const hx_group_desc& g, int nodes_per_warp, int max_pack_
         cap = std::min(cap, max_pack_nodes);
     }
     cap = std::max(cap, maxcell);
-    std::vector<int> wc(ncell);
-    for (int c = 0; c < ncell; c++) wc[c] = std::min(kWarpsPerCta, std::max(1, (cell_size[c] + npw - 1) / npw));
+    std::vector<int> wc(ncell, 1);
     std::vector<int> order(ncell);
     std::iota(order.begin(), order.end(), 0);
     std::stable_sort(order.begin(), order.end(), [&](int x, int y) { return cell_size[x] > cell_size[y]; });
     std::vector<std::vector<int>> bins;
-    std::vector<int> bin_w, bin_n;
+    std::vector<int> bin_n;
     for (int c : order) {
         int b = -1;
         for (int k = 0; k < (int)bins.size(); k++)
-            if (bin_w[k] + wc[c] <= kWarpsPerCta && bin_n[k] + cell_size[c] <= cap) {
+            if ((int)bins[k].size() < kWarpsPerCta && bin_n[k] + cell_size[c] <= cap) {
                 b = k;
                 break;
             }
         if (b < 0) {
             bins.push_back({});
-            bin_w.push_back(0);
             bin_n.push_back(0);
             b = (int)bins.size() - 1;
         }
         bins[b].push_back(c);
-        bin_w[b] += wc[c];
         bin_n[b] += cell_size[c];
     }
-    // hand the spare warps of each CTA to its cells with the most nodes per warp
     for (size_t b = 0; b < bins.size(); b++) {
-        int spare = kWarpsPerCta - bin_w[b];
-        while (spare > 0) {
+        const int nb = (int)bins[b].size();
+        const double tot = (double)bin_n[b];
+        int used = 0;
+        std::vector<std::pair<double, int>> rem;
+        for (int c : bins[b]) {
+            const double share = kWarpsPerCta * (double)cell_size[c] / tot;
+            wc[c] = std::max(1, (int)std::floor(share));
+            used += wc[c];
+            rem.push_back({share - std::floor(share), c});
+        }
+        // hand out the rest by largest remainder (then most nodes per warp)
+        std::stable_sort(rem.begin(), rem.end(), [&](const std::pair<double, int>& x, const std::pair<double, int>& y) {
+            return x.first > y.first;
+        });
+        for (size_t i = 0; used < kWarpsPerCta && nb > 0; i = (i + 1) % rem.size()) {
+            wc[rem[i].second]++;
+            used++;
+        }
+        // floor-at-one may have overshot for packs of many small cells: take warps
+        // back from the cells with the fewest nodes per warp
+        while (used > kWarpsPerCta) {
             int best = -1;
-            double bestv = -1;
+            double bv = 1e300;
             for (int c : bins[b]) {
                 double v = (double)cell_size[c] / wc[c];
-                if (wc[c] < kWarpsPerCta && v > bestv) {
-                    bestv = v;
+                if (wc[c] > 1 && v < bv) {
+                    bv = v;
                     best = c;
                 }
             }
             if (best < 0) break;
-            wc[best]++;
-            spare--;
+            wc[best]--;
+            used--;
         }
         std::sort(bins[b].begin(), bins[b].end());
     }

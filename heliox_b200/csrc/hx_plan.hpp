@@ -24,7 +24,7 @@
 
 namespace hx {
 
-constexpr int kWarpsPerCta = 8;
+constexpr int kWarpsPerCta = 16;
 
 struct Plan {
     int ncell = 0, nnode = 0, nhh = 0, npas = 0, nic = 0;

@@ -250,9 +250,31 @@ int hx_load_group(hx_ctx* ctx, const hx_group_desc* desc) {
     // doubles per node plus the topology tables, about 16 bytes per node)
     int optin = 0;
     HXC(cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, ctx->device));
-    const int cap_nodes = (int)((optin - 4096) / (10 * sizeof(double) + 20));
+    // (network groups: plus 2 doubles per synapse in the pack, budgeted at 1.5x
+    // the group's mean synapse density; a pack that still overflows shrinks the cap)
+    const double syn_per_node =
+        desc->nnode > 0 ? (double)(std::max(desc->nexpsyn, 0) + std::max(desc->nexp2syn, 0)) / desc->nnode : 0.0;
+    int cap_nodes = (int)((optin - 4096) / (10 * sizeof(double) + 20 + 1.5 * 16 * syn_per_node));
     std::string e = hx::build_plan(*desc, ctx->pack_target, cap_nodes, ctx->P);
     if (!e.empty()) return fail(ctx, "invalid group: " + e);
+    for (int shrink = 0; shrink < 6 && desc->nnode > 0; shrink++) {
+        // largest synapse count of any pack under this plan
+        const hx::Plan& Pc = ctx->P;
+        std::vector<int> nsyn_node(Pc.nnode, 0);
+        for (int i = 0; i < std::max(desc->nexpsyn, 0); i++) nsyn_node[Pc.ref2gpu[desc->expsyn_node[i]]]++;
+        for (int i = 0; i < std::max(desc->nexp2syn, 0); i++) nsyn_node[Pc.ref2gpu[desc->exp2syn_node[i]]]++;
+        int worst = 0;
+        for (int p = 0; p < Pc.npack; p++) {
+            int s = 0;
+            for (int gi = Pc.pack_node_off[p]; gi < Pc.pack_node_off[p + 1]; gi++) s += nsyn_node[gi];
+            worst = std::max(worst, s);
+        }
+        const size_t need = (size_t)Pc.max_pack_nodes * (10 * sizeof(double) + 20) + 16 * (size_t)worst + 4096;
+        if (need <= (size_t)optin) break;
+        cap_nodes = (int)(cap_nodes * 0.9);
+        e = hx::build_plan(*desc, ctx->pack_target, cap_nodes, ctx->P);
+        if (!e.empty()) return fail(ctx, "invalid group: " + e);
+    }
     const hx::Plan& P = ctx->P;
     cudaStream_t st = ctx->st;
     const size_t nn = P.nnode, nc = P.nic;
