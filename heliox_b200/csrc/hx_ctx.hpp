@@ -152,6 +152,13 @@ struct hx_ctx {
     void* exchange_user = nullptr;
     int nranks = 1;
     size_t ck_net_stride = 0;  // doubles per checkpoint beyond v, m, h, n
+
+    // ---- a cell split across CTAs (hx_split.cu)
+    bool split = false;
+    hx::DevSplit X{};
+    DevBuf<int> sub_root, sub_parent, split_err;
+    DevBuf<double> xd, xrhs, xx, xv, xvp;
+    DevBuf<unsigned> split_bar;
 };
 
 // The runtime's own error path (sets hx_last_error, returns -1).

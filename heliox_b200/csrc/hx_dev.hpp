@@ -64,6 +64,21 @@ struct DevGrad {
     double *hg_g, *gj_g, *gj_w, *gr_w;  // HalfGap, gapjunction_lr, neuron_to_neuron_syn_lr
 };
 
+// A cell split across CTAs (hx_plan.hpp): pack 0 holds the top part, the
+// other packs its subtrees.  Per subtree id, the interface values that cross
+// CTAs each step go through these arrays; the grid barrier counter lives in
+// bar[0..1] and err records a barrier that gave up waiting.
+struct DevSplit {
+    int nsub, nblocks;
+    const int *sub_root, *sub_parent;  // GPU node ids
+    double *xd, *xrhs;                 // eliminated diagonal / rhs of each subtree root
+    double *xx;                        // solution at each root's parent (dv forward, w backward)
+    double *xv;                        // root value read by the top part (v forward, w backward)
+    double *xvp;                       // v of each root's parent (forward)
+    unsigned* bar;
+    int* err;
+};
+
 // Network parts of a group (step kernels instantiated with kNet = true).
 // Instance arrays are in GPU order: sorted by GPU node, ExpSyn before Exp2Syn
 // on a node, then by reference instance -- the order in which the reference's

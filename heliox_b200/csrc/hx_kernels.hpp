@@ -17,6 +17,15 @@ cudaError_t launch_fwd(const DevGroup& G, const DevState& S, const DevTape& T, i
 cudaError_t launch_bwd(const DevGroup& G, const DevTape& T, const DevAdj& A, const DevGrad& GR, const DevProbe& P,
                        const double* dLdv, const double* tmid, int k_hi, int k_lo, cudaStream_t st,
                        const DevNet* N = nullptr);
+// split cell (hx_split.cu): cooperative launches over all packs
+cudaError_t configure_split(size_t smem_fwd, size_t smem_bwd);
+const void* split_fwd_kernel_ptr();
+const void* split_bwd_kernel_ptr();
+cudaError_t launch_split_fwd(const DevGroup& G, const DevState& S, const DevTape& T, int write_tape, const DevProbe& P,
+                             double* trace, const double* tmid, int k0, int k1, const DevSplit& X, cudaStream_t st);
+cudaError_t launch_split_bwd(const DevGroup& G, const DevTape& T, const DevAdj& A, const DevGrad& GR, const DevProbe& P,
+                             const double* dLdv, const double* tmid, int k_hi, int k_lo, const DevSplit& X,
+                             cudaStream_t st);
 cudaError_t launch_syn_prep(int n, const int* kind, const double* tau1, const double* tau2, double dt, double* cA,
                             double* cB, double* fA, double* fB, cudaStream_t st);
 cudaError_t launch_init_net(int nsyn, double* sA, double* sB, int ngr, const double* gr_w, const double* gr_vth,

@@ -7,6 +7,7 @@
 #include <numeric>
 #include <queue>
 #include <sstream>
+#include <unordered_map>
 
 namespace hx {
 
@@ -52,6 +53,93 @@ std::string validate(const hx_group_desc& g) {
     if (g.npas && (!g.pas_g || !g.pas_e)) return "pas: missing parameter arrays";
     if (!(r = chk(g.nic, g.ic_node, false, "IClamp")).empty()) return r;
     if (g.nic && (!g.ic_del || !g.ic_dur || !g.ic_amp)) return "IClamp: missing parameter arrays";
+    return "";
+}
+
+// Splits one cell's branches into a top unit and subtree units of at most
+// cap nodes each: starting from the root branch, the branch whose subtree is
+// largest among those hanging off the top unit moves into it until every
+// hanging subtree fits.  Branch levels and parent links are renumbered per unit.
+std::string split_cell(const std::vector<Branch>& Bin, const std::vector<int>& parent_ref, int cap,
+                       std::vector<std::vector<Branch>>& units) {
+    // parent branches from the node structure (the branch list is sorted by
+    // level and head, so parent indices recorded while building it are stale)
+    std::vector<Branch> B = Bin;
+    const int nb = (int)B.size();
+    {
+        std::unordered_map<int, int> br_of;
+        for (int i = 0; i < nb; i++)
+            for (int r : B[i].nodes) br_of[r] = i;
+        for (int i = 0; i < nb; i++) {
+            const int pr = parent_ref[B[i].head_ref];
+            B[i].parent_branch = pr < 0 ? -1 : br_of[pr];
+        }
+    }
+    std::vector<std::vector<int>> kids(nb);
+    for (int i = 0; i < nb; i++)
+        if (B[i].parent_branch >= 0) kids[B[i].parent_branch].push_back(i);
+    std::vector<long long> sub(nb, 0);
+    for (int i = nb - 1; i >= 0; i--) {  // sorted by level: children after parents
+        sub[i] += (long long)B[i].nodes.size();
+        if (B[i].parent_branch >= 0) sub[B[i].parent_branch] += sub[i];
+    }
+    std::vector<char> top(nb, 0);
+    top[0] = 1;
+    long long top_nodes = (long long)B[0].nodes.size();
+    for (;;) {
+        int worst = -1;
+        for (int i = 1; i < nb; i++)
+            if (!top[i] && top[B[i].parent_branch] && (worst < 0 || sub[i] > sub[worst])) worst = i;
+        if (worst < 0 || sub[worst] <= cap) break;
+        top[worst] = 1;
+        top_nodes += (long long)B[worst].nodes.size();
+        if (top_nodes > cap) return "cell too large to split into CTA-sized parts";
+    }
+    units.clear();
+    auto emit = [&](const std::vector<int>& members) {
+        std::vector<Branch> U;
+        std::vector<int> local(nb, -1);
+        for (int i : members) {
+            Branch br = B[i];
+            const int pb = B[i].parent_branch;
+            br.parent_branch = (pb >= 0 && local[pb] >= 0) ? local[pb] : -1;
+            br.level = br.parent_branch < 0 ? 0 : U[br.parent_branch].level + 1;
+            local[i] = (int)U.size();
+            U.push_back(std::move(br));
+        }
+        std::vector<int> idx(U.size());
+        std::iota(idx.begin(), idx.end(), 0);
+        std::stable_sort(idx.begin(), idx.end(), [&](int x, int y) {
+            if (U[x].level != U[y].level) return U[x].level < U[y].level;
+            return U[x].head_ref < U[y].head_ref;
+        });
+        std::vector<int> pos(U.size());
+        for (size_t k = 0; k < idx.size(); k++) pos[idx[k]] = (int)k;
+        std::vector<Branch> S;
+        for (int k : idx) {
+            Branch br = U[k];
+            if (br.parent_branch >= 0) br.parent_branch = pos[br.parent_branch];
+            S.push_back(std::move(br));
+        }
+        units.push_back(std::move(S));
+    };
+    std::vector<int> tm;
+    for (int i = 0; i < nb; i++)
+        if (top[i]) tm.push_back(i);
+    emit(tm);
+    for (int r = 1; r < nb; r++) {
+        if (top[r] || !top[B[r].parent_branch]) continue;
+        std::vector<int> m;  // the subtree of r in BFS order
+        std::queue<int> q;
+        q.push(r);
+        while (!q.empty()) {
+            int i = q.front();
+            q.pop();
+            m.push_back(i);
+            for (int c : kids[i]) q.push(c);
+        }
+        emit(m);
+    }
     return "";
 }
 
@@ -117,13 +205,41 @@ std::string build_plan(const hx_group_desc& g, int nodes_per_warp, int max_pack_
         });
     }
 
+    // units: one per cell, unless a single cell exceeds the per-CTA capacity,
+    // in which case it is split into a top unit (containing the root) and
+    // subtree units hanging off it (see split_cell)
+    std::vector<std::vector<Branch>> ubr;
+    std::vector<int> usize, ucell;
+    int top_unit = -1;
+    {
+        const int cap_guess = max_pack_nodes > 0 ? max_pack_nodes : 0;
+        const int maxc = *std::max_element(cell_size.begin(), cell_size.end());
+        if (cap_guess > 0 && maxc > cap_guess) {
+            if (ncell != 1) return "a cell exceeds the per-CTA capacity; only a group of one cell can be split";
+            std::string se = split_cell(cbr[0], std::vector<int>(g.parent, g.parent + n), cap_guess, ubr);
+            if (!se.empty()) return se;
+            top_unit = 0;
+            for (auto& B : ubr) {
+                int sz = 0;
+                for (auto& br : B) sz += (int)br.nodes.size();
+                usize.push_back(sz);
+                ucell.push_back(0);
+            }
+        } else {
+            ubr = cbr;
+            usize = cell_size;
+            for (int c = 0; c < ncell; c++) ucell.push_back(c);
+        }
+    }
+    const int nunit = (int)ubr.size();
+
     // first-fit-decreasing packing of whole cells into CTAs by node count (the
     // shared-memory capacity; at most kWarpsPerCta cells), then the CTA's warps
     // are shared among its cells in proportion to their nodes (at least one
     // each, largest remainders first), so every thread of a CTA carries about
     // the same number of nodes.
     const int npw = nodes_per_warp > 0 ? nodes_per_warp : 144;
-    const int maxcell = *std::max_element(cell_size.begin(), cell_size.end());
+    const int maxcell = *std::max_element(usize.begin(), usize.end());
     int cap = npw * kWarpsPerCta;
     if (max_pack_nodes > 0) {
         if (maxcell > max_pack_nodes)
@@ -132,16 +248,21 @@ std::string build_plan(const hx_group_desc& g, int nodes_per_warp, int max_pack_
         cap = std::min(cap, max_pack_nodes);
     }
     cap = std::max(cap, maxcell);
-    std::vector<int> wc(ncell, 1);
-    std::vector<int> order(ncell);
-    std::iota(order.begin(), order.end(), 0);
-    std::stable_sort(order.begin(), order.end(), [&](int x, int y) { return cell_size[x] > cell_size[y]; });
+    std::vector<int> wc(nunit, 1);
+    std::vector<int> order;
+    for (int u = 0; u < nunit; u++)
+        if (u != top_unit) order.push_back(u);
+    std::stable_sort(order.begin(), order.end(), [&](int x, int y) { return usize[x] > usize[y]; });
     std::vector<std::vector<int>> bins;
     std::vector<int> bin_n;
+    if (top_unit >= 0) {  // the top unit has a CTA of its own (pack 0)
+        bins.push_back({top_unit});
+        bin_n.push_back(usize[top_unit]);
+    }
     for (int c : order) {
         int b = -1;
-        for (int k = 0; k < (int)bins.size(); k++)
-            if ((int)bins[k].size() < kWarpsPerCta && bin_n[k] + cell_size[c] <= cap) {
+        for (int k = top_unit >= 0 ? 1 : 0; k < (int)bins.size(); k++)
+            if ((int)bins[k].size() < kWarpsPerCta && bin_n[k] + usize[c] <= cap) {
                 b = k;
                 break;
             }
@@ -151,7 +272,7 @@ std::string build_plan(const hx_group_desc& g, int nodes_per_warp, int max_pack_
             b = (int)bins.size() - 1;
         }
         bins[b].push_back(c);
-        bin_n[b] += cell_size[c];
+        bin_n[b] += usize[c];
     }
     for (size_t b = 0; b < bins.size(); b++) {
         const int nb = (int)bins[b].size();
@@ -159,7 +280,7 @@ std::string build_plan(const hx_group_desc& g, int nodes_per_warp, int max_pack_
         int used = 0;
         std::vector<std::pair<double, int>> rem;
         for (int c : bins[b]) {
-            const double share = kWarpsPerCta * (double)cell_size[c] / tot;
+            const double share = kWarpsPerCta * (double)usize[c] / tot;
             wc[c] = std::max(1, (int)std::floor(share));
             used += wc[c];
             rem.push_back({share - std::floor(share), c});
@@ -178,7 +299,7 @@ std::string build_plan(const hx_group_desc& g, int nodes_per_warp, int max_pack_
             int best = -1;
             double bv = 1e300;
             for (int c : bins[b]) {
-                double v = (double)cell_size[c] / wc[c];
+                double v = (double)usize[c] / wc[c];
                 if (wc[c] > 1 && v < bv) {
                     bv = v;
                     best = c;
@@ -216,10 +337,10 @@ std::string build_plan(const hx_group_desc& g, int nodes_per_warp, int max_pack_
         int wpos = 0, bar = 1, brl = 0;
         int pack_levels = 0, crit = 0;
         for (int c : bins[p]) {
-            const std::vector<Branch>& B = cbr[c];
-            P.cs_cell.push_back(c);
+            const std::vector<Branch>& B = ubr[c];
+            P.cs_cell.push_back(ucell[c]);
             P.cs_node0.push_back(gpos - base);
-            P.cs_nnode.push_back(cell_size[c]);
+            P.cs_nnode.push_back(usize[c]);
             P.cs_warp0.push_back(wpos);
             P.cs_nwarp.push_back(wc[c]);
             P.cs_bar.push_back(wc[c] > 1 ? bar++ : 0);
@@ -237,13 +358,13 @@ std::string build_plan(const hx_group_desc& g, int nodes_per_warp, int max_pack_
                 for (int ref : br.nodes) {
                     P.gpu2ref[gpos] = ref;
                     P.ref2gpu[ref] = gpos;
-                    P.node_cell[gpos] = c;
+                    P.node_cell[gpos] = ucell[c];
                     gpos++;
                 }
         }
         // branches of the pack (cell by cell, already level-sorted)
         for (int c : bins[p])
-            for (const Branch& br : cbr[c]) {
+            for (const Branch& br : ubr[c]) {
                 P.br_head.push_back(P.ref2gpu[br.head_ref] - base);
                 P.br_end.push_back(P.ref2gpu[br.end_ref] - base);
                 int hp = g.parent[br.head_ref];
@@ -259,7 +380,8 @@ std::string build_plan(const hx_group_desc& g, int nodes_per_warp, int max_pack_
             std::vector<int> depth(pn, 0);
             for (int l = 0; l < pn; l++) {
                 int pr = g.parent[P.gpu2ref[base + l]];
-                depth[l] = pr < 0 ? 1 : depth[P.ref2gpu[pr] - base] + 1;
+                const int pl = pr < 0 ? -1 : P.ref2gpu[pr] - base;
+                depth[l] = (pl < 0 || pl >= l) ? 1 : depth[pl] + 1;
                 crit = std::max(crit, depth[l]);
             }
         }
@@ -283,6 +405,51 @@ std::string build_plan(const hx_group_desc& g, int nodes_per_warp, int max_pack_
         P.max_pack_nch = std::max(P.max_pack_nch, P.pack_nch_off[p + 1] - P.pack_nch_off[p]);
     }
     P.imbalance = (double)P.max_pack_nodes / ((double)sum_nodes / (double)npack);
+    if (top_unit >= 0) {
+        // links between the top unit (pack 0) and the subtree units: the
+        // subtree roots' parents, the top nodes' children and branch children
+        // in other packs are written as -(2 + subtree id)
+        std::vector<int> pack_of(n);
+        for (int p = 0; p < npack; p++)
+            for (int gi = P.pack_node_off[p]; gi < P.pack_node_off[p + 1]; gi++) pack_of[gi] = p;
+        std::vector<int> sub_of_root(n, -1);
+        for (int p = 1; p < npack; p++)
+            for (int s2 = P.pack_slot_off[p]; s2 < P.pack_slot_off[p + 1]; s2++) {
+                const int root = P.pack_node_off[p] + P.cs_node0[s2];
+                const int id = (int)P.sub_root.size();
+                sub_of_root[root] = id;
+                P.sub_root.push_back(root);
+                P.sub_parent.push_back(P.ref2gpu[g.parent[P.gpu2ref[root]]]);
+            }
+        P.nsub = (int)P.sub_root.size();
+        auto code = [&](int gi_other, int p, int base) {
+            return pack_of[gi_other] == p ? gi_other - base : -(2 + sub_of_root[gi_other]);
+        };
+        for (int p = 0; p < npack; p++) {
+            const int base = P.pack_node_off[p];
+            // a subtree root's parent link carries the subtree's own id
+            for (int gi = base; gi < P.pack_node_off[p + 1]; gi++) {
+                const int pr = g.parent[P.gpu2ref[gi]];
+                if (pr >= 0)
+                    P.node_parent[gi] = pack_of[P.ref2gpu[pr]] == p ? P.ref2gpu[pr] - base : -(2 + sub_of_root[gi]);
+            }
+            // children lists rebuilt in their original orders with final indices
+            int k = P.pack_nch_off[p];
+            for (int gi = base; gi < P.pack_node_off[p + 1]; gi++) {
+                const int ref = P.gpu2ref[gi];
+                for (int c = child_off[ref]; c < child_off[ref + 1]; c++) P.node_child[k++] = code(P.ref2gpu[child[c]], p, base);
+            }
+            for (int b = P.pack_br_off[p]; b < P.pack_br_off[p + 1]; b++) {
+                const int hg = P.br_head[b] + base, hr = P.gpu2ref[hg];
+                P.br_parent[b] = g.parent[hr] < 0 ? -1
+                                 : pack_of[P.ref2gpu[g.parent[hr]]] == p ? P.ref2gpu[g.parent[hr]] - base
+                                                                         : -(2 + sub_of_root[hg]);
+                const int er = P.gpu2ref[P.br_end[b] + base];
+                int kk = P.br_child_off[b];
+                for (int c = child_off[er + 1] - 1; c >= child_off[er]; c--) P.br_child[kk++] = code(P.ref2gpu[child[c]], p, base);
+            }
+        }
+    }
     P.node_child_off.assign(n + 1, 0);
     {
         int k = 0;
@@ -320,21 +487,42 @@ std::string build_plan(const hx_group_desc& g, int nodes_per_warp, int max_pack_
     return "";
 }
 
-// Replays the schedule: per pack, per cell slot, levels deepest-first then root-first.
+// Replays the schedule: per pack, per cell slot, levels deepest-first then
+// root-first.  For a split cell the triangularisation visits the subtree
+// packs before the top pack (pack 0) and the back-substitution the top pack
+// first, as the kernels' grid barriers order them.
 template <class Tri, class Back>
 static void walk_schedule(const Plan& P, Tri tri, Back back) {
-    for (int p = 0; p < P.npack; p++) {
+    auto run = [&](int p, bool do_tri) {
         const int base = P.pack_node_off[p];
         const int bbase = P.pack_br_off[p];
         for (int s = P.pack_slot_off[p]; s < P.pack_slot_off[p + 1]; s++) {
             const int* lo = &P.level_br_off[P.cs_lvl_off[s]];
             const int nlev = P.cs_nlev[s];
-            for (int L = nlev - 1; L >= 0; L--)
-                for (int br = lo[L]; br < lo[L + 1]; br++) tri(base, bbase + br);
-            for (int L = 0; L < nlev; L++)
-                for (int br = lo[L]; br < lo[L + 1]; br++) back(base, bbase + br);
+            if (do_tri) {
+                for (int L = nlev - 1; L >= 0; L--)
+                    for (int br = lo[L]; br < lo[L + 1]; br++) tri(base, bbase + br);
+            } else {
+                for (int L = 0; L < nlev; L++)
+                    for (int br = lo[L]; br < lo[L + 1]; br++) back(base, bbase + br);
+            }
         }
+    };
+    if (P.nsub > 0) {
+        for (int p = P.npack - 1; p >= 0; p--) run(p, true);
+        for (int p = 0; p < P.npack; p++) run(p, false);
+        return;
     }
+    for (int p = 0; p < P.npack; p++) {
+        run(p, true);
+        run(p, false);
+    }
+}
+
+// global GPU index of a branch child / branch parent entry (codes of a split cell)
+static inline int child_global(const Plan& P, int base, int c) { return c >= 0 ? base + c : P.sub_root[-c - 2]; }
+static inline int parent_global(const Plan& P, int base, int c) {
+    return c >= 0 ? base + c : (c == -1 ? -1 : P.sub_parent[-c - 2]);
 }
 
 void planned_solve_cpu(const Plan& P, const double* a, const double* b, double* d, double* rhs, bool transposed) {
@@ -343,38 +531,28 @@ void planned_solve_cpu(const Plan& P, const double* a, const double* b, double* 
     walk_schedule(
         P,
         [&](int base, int gb) {
-            double* dd = d + base;
-            double* rr = rhs + base;
-            const double* AA = A + base;
-            const double* UU = U + base;
-            const int h = P.br_head[gb], e = P.br_end[gb];
+            const int h = base + P.br_head[gb], e = base + P.br_end[gb];
+            // children of the end node, descending reference index
             for (int k = P.br_child_off[gb]; k < P.br_child_off[gb + 1]; k++) {
-                const int c = P.br_child[k];
-                double f = AA[c] / dd[c];
-                dd[e] -= f * UU[c];
-                rr[e] -= f * rr[c];
+                const int c = child_global(P, base, P.br_child[k]);
+                double pp = A[c] / d[c];
+                d[e] -= pp * U[c];
+                rhs[e] -= pp * rhs[c];
             }
             for (int j = e; j > h; j--) {
-                double f = AA[j] / dd[j];
-                dd[j - 1] -= f * UU[j];
-                rr[j - 1] -= f * rr[j];
+                double pp = A[j] / d[j];
+                d[j - 1] -= pp * U[j];
+                rhs[j - 1] -= pp * rhs[j];
             }
         },
         [&](int base, int gb) {
-            double* dd = d + base;
-            double* rr = rhs + base;
-            const double* UU = U + base;
-            const int h = P.br_head[gb], e = P.br_end[gb];
-            const int par = P.br_parent[gb];
-            if (par < 0) {
-                rr[h] /= dd[h];
-            } else {
-                rr[h] -= UU[h] * rr[par];
-                rr[h] /= dd[h];
-            }
+            const int h = base + P.br_head[gb], e = base + P.br_end[gb];
+            const int par = parent_global(P, base, P.br_parent[gb]);
+            if (par >= 0) rhs[h] -= U[h] * rhs[par];
+            rhs[h] /= d[h];
             for (int j = h + 1; j <= e; j++) {
-                rr[j] -= UU[j] * rr[j - 1];
-                rr[j] /= dd[j];
+                rhs[j] -= U[j] * rhs[j - 1];
+                rhs[j] /= d[j];
             }
         });
 }
@@ -385,24 +563,20 @@ void planned_solve_pq_cpu(const Plan& P, const double* a, const double* b, doubl
     walk_schedule(
         P,
         [&](int base, int gb) {
-            double* dd = d + base;
-            double* rr = rhs + base;
-            const double* AA = A + base;
-            const double* UU = U + base;
-            const int h = P.br_head[gb], e = P.br_end[gb];
-            double de = dd[e], re = rr[e];
+            const int h = base + P.br_head[gb], e = base + P.br_end[gb];
+            double de = d[e], re = rhs[e];
             for (int k = P.br_child_off[gb]; k < P.br_child_off[gb + 1]; k++) {
-                const int c = P.br_child[k];
-                de = std::fma(-(AA[c] * UU[c]), dd[c], de);
-                re = std::fma(-AA[c], rr[c], re);
+                const int c = child_global(P, base, P.br_child[k]);
+                de = std::fma(-(A[c] * U[c]), d[c], de);
+                re = std::fma(-A[c], rhs[c], re);
             }
             double pp = de, qq = 1.0, yy = re;
             for (int j = e; j > h; j--) {
-                const double pn = std::fma(dd[j - 1], pp, -((AA[j] * UU[j]) * qq));
-                const double yn = std::fma(rr[j - 1], pp, -(AA[j] * yy));
+                const double pn = std::fma(d[j - 1], pp, -((A[j] * U[j]) * qq));
+                const double yn = std::fma(rhs[j - 1], pp, -(A[j] * yy));
                 const double ip = 1.0 / pp;
-                dd[j] = qq * ip;
-                rr[j] = yy * ip;
+                d[j] = qq * ip;
+                rhs[j] = yy * ip;
                 qq = pp;
                 pp = pn;
                 yy = yn;
@@ -414,21 +588,18 @@ void planned_solve_pq_cpu(const Plan& P, const double* a, const double* b, doubl
                 }
             }
             const double ip = 1.0 / pp;
-            dd[h] = qq * ip;
-            rr[h] = yy * ip;
+            d[h] = qq * ip;
+            rhs[h] = yy * ip;
         },
         [&](int base, int gb) {
-            double* dd = d + base;
-            double* rr = rhs + base;
-            const double* UU = U + base;
-            const int h = P.br_head[gb], e = P.br_end[gb];
-            const int par = P.br_parent[gb];
-            double x = rr[h];
-            if (par >= 0) x = std::fma(-(UU[h] * dd[h]), rr[par], x);
-            rr[h] = x;
+            const int h = base + P.br_head[gb], e = base + P.br_end[gb];
+            const int par = parent_global(P, base, P.br_parent[gb]);
+            double x = rhs[h];
+            if (par >= 0) x = std::fma(-(U[h] * d[h]), rhs[par], x);
+            rhs[h] = x;
             for (int j = h + 1; j <= e; j++) {
-                x = std::fma(-(UU[j] * dd[j]), x, rr[j]);
-                rr[j] = x;
+                x = std::fma(-(U[j] * d[j]), x, rhs[j]);
+                rhs[j] = x;
             }
         });
 }

@@ -57,6 +57,12 @@ struct Plan {
     std::vector<int> node_ic;          // GPU IClamp instance ids
     std::vector<int> ic_gpu2ref;
     std::vector<int> node_cell;        // GPU node -> cell id
+    // split cell (one cell larger than a CTA): pack 0 holds the top unit, the
+    // other packs hold subtree units; links between them are coded in
+    // node_parent / node_child / br_parent / br_child as -(2 + subtree id)
+    int nsub = 0;
+    std::vector<int> sub_root;    // GPU node of each subtree root
+    std::vector<int> sub_parent;  // GPU node (in pack 0) of its parent
     // statistics
     int max_pack_nodes = 0, max_pack_hh = 0, max_levels = 0, max_crit = 0;
     int max_pack_branches = 0, max_pack_bch = 0, max_pack_nch = 0;

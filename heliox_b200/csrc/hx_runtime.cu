@@ -111,6 +111,7 @@ static void fill_stats(const hx::Plan& P, hx_plan_stats* out) {
     out->max_crit_nodes = P.max_crit;
     out->nbranch = (int)P.br_head.size();
     out->imbalance = P.imbalance;
+    out->nsub = P.nsub;
     plan_smem(P, out->smem_fwd, out->smem_bwd);
 }
 
@@ -177,9 +178,14 @@ int hx_set_tape_budget(hx_ctx* ctx, size_t bytes) {
 
 int hx_plan_check(const hx_group_desc* desc, int nodes_per_warp, hx_plan_stats* out, double* max_abs_diff,
                   double* pq_rel_diff) {
+    return hx_plan_check_cap(desc, nodes_per_warp, 0, out, max_abs_diff, pq_rel_diff);
+}
+
+int hx_plan_check_cap(const hx_group_desc* desc, int nodes_per_warp, int max_pack_nodes, hx_plan_stats* out,
+                      double* max_abs_diff, double* pq_rel_diff) {
     if (!desc) return -1;
     hx::Plan P;
-    std::string e = hx::build_plan(*desc, nodes_per_warp, 0, P);
+    std::string e = hx::build_plan(*desc, nodes_per_warp, max_pack_nodes, P);
     if (!e.empty()) {
         fprintf(stderr, "hx_plan_check: %s\n", e.c_str());
         return -2;
@@ -431,6 +437,36 @@ int hx_load_group(hx_ctx* ctx, const hx_group_desc* desc) {
         return fail(ctx, "cell pack needs " + std::to_string(need) + " B shared memory (> " + std::to_string(maxsmem) +
                              "); lower the pack target or split the cell");
     HXC(hx::configure_kernels(sf, sb, std::min(sfn, (size_t)maxsmem), std::min(sbn, (size_t)maxsmem)));
+    ctx->split = P.nsub > 0;
+    if (ctx->split) {
+        if (ctx->net) return fail(ctx, "a cell split across CTAs cannot carry network parts");
+        HXC(hx::configure_split(sf, sb));
+        int per_sm = 0, nsm = 0;
+        HXC(cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, ctx->device));
+        int per_sm_b = 0;
+        HXC(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, hx::split_fwd_kernel_ptr(), hx::kThreads, sf));
+        HXC(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm_b, hx::split_bwd_kernel_ptr(), hx::kThreads, sb));
+        if ((long long)std::min(per_sm, per_sm_b) * nsm < P.npack)
+            return fail(ctx, "split cell needs " + std::to_string(P.npack) + " co-resident CTAs (have " +
+                                 std::to_string(std::min(per_sm, per_sm_b) * nsm) + ")");
+        HXC(ctx->sub_root.upload(P.sub_root, st));
+        HXC(ctx->sub_parent.upload(P.sub_parent, st));
+        for (auto* b : {&ctx->xd, &ctx->xrhs, &ctx->xx, &ctx->xv, &ctx->xvp}) HXC(b->ensure(P.nsub));
+        HXC(ctx->split_bar.ensure(2));
+        HXC(ctx->split_err.ensure(1));
+        hx::DevSplit& X = ctx->X;
+        X.nsub = P.nsub;
+        X.nblocks = P.npack;
+        X.sub_root = ctx->sub_root.p;
+        X.sub_parent = ctx->sub_parent.p;
+        X.xd = ctx->xd.p;
+        X.xrhs = ctx->xrhs.p;
+        X.xx = ctx->xx.p;
+        X.xv = ctx->xv.p;
+        X.xvp = ctx->xvp.p;
+        X.bar = ctx->split_bar.p;
+        X.err = ctx->split_err.p;
+    }
     {
         std::vector<double*> ptrs(HX_P_COUNT);
         for (int k = 0; k < HX_P_COUNT; k++) ptrs[k] = hx_kind_ptr(ctx, k);
@@ -598,6 +634,33 @@ static int copy_ck(hx_ctx* ctx, int s, bool save) {
     return 0;
 }
 
+// plain or split-cell kernels (the split ones reset their barrier state per launch)
+static cudaError_t fwd_launch(hx_ctx* ctx, const hx::DevState& S, const hx::DevTape& T, int write_tape,
+                              const hx::DevProbe& PV, double* trace, int k0, int k1) {
+    if (!ctx->split) return hx::launch_fwd(ctx->G, S, T, write_tape, PV, trace, ctx->tmid.p, k0, k1, ctx->st);
+    cudaError_t e = cudaMemsetAsync(ctx->split_bar.p, 0, 2 * sizeof(unsigned), ctx->st);
+    if (e != cudaSuccess) return e;
+    return hx::launch_split_fwd(ctx->G, S, T, write_tape, PV, trace, ctx->tmid.p, k0, k1, ctx->X, ctx->st);
+}
+
+static cudaError_t bwd_launch(hx_ctx* ctx, const hx::DevTape& T, const hx::DevAdj& A, const hx::DevGrad& GR,
+                              const hx::DevProbe& PV, const double* dLdv, int k_hi, int k_lo) {
+    if (!ctx->split) return hx::launch_bwd(ctx->G, T, A, GR, PV, dLdv, ctx->tmid.p, k_hi, k_lo, ctx->st);
+    cudaError_t e = cudaMemsetAsync(ctx->split_bar.p, 0, 2 * sizeof(unsigned), ctx->st);
+    if (e != cudaSuccess) return e;
+    return hx::launch_split_bwd(ctx->G, T, A, GR, PV, dLdv, ctx->tmid.p, k_hi, k_lo, ctx->X, ctx->st);
+}
+
+// a split-cell grid barrier that gave up waiting (the results are then invalid)
+static int check_split(hx_ctx* ctx) {
+    if (!ctx->split) return 0;
+    int err = 0;
+    HXC(cudaMemcpyAsync(&err, ctx->split_err.p, 4, cudaMemcpyDeviceToHost, ctx->st));
+    HXC(cudaStreamSynchronize(ctx->st));
+    if (err) return fail(ctx, "a grid barrier of the split-cell kernels timed out");
+    return 0;
+}
+
 static int run_forward(hx_ctx* ctx, int nstep, double v_init, int nprobe, const int* probe, double* trace_dev,
                        bool capture) {
     if (!ctx->loaded) return fail(ctx, "no group loaded");
@@ -614,20 +677,22 @@ static int run_forward(hx_ctx* ctx, int nstep, double v_init, int nprobe, const 
     hx::DevState S = state_view(ctx);
     hx::DevProbe PV = hx_probe_view(ctx);
     HXC(hx::launch_init(ctx->G, S, v_init, ctx->st));
+    if (ctx->split) HXC(cudaMemsetAsync(ctx->split_err.p, 0, 4, ctx->st));
     HXC(cudaEventRecord(ctx->ev[0], ctx->st));
     int launches = 0;
     if (!capture || ctx->full_tape) {
-        HXC(hx::launch_fwd(ctx->G, S, T, capture ? 1 : 0, PV, trace_dev, ctx->tmid.p, 0, nstep, ctx->st));
+        HXC(fwd_launch(ctx, S, T, capture ? 1 : 0, PV, trace_dev, 0, nstep));
         launches = 1;
     } else {
         for (int s = 0; s < ctx->nseg; s++) {
             if (copy_ck(ctx, s, true)) return -1;
             int k0 = s * ctx->seg, k1 = std::min(nstep, k0 + ctx->seg);
-            HXC(hx::launch_fwd(ctx->G, S, T, 0, PV, trace_dev, ctx->tmid.p, k0, k1, ctx->st));
+            HXC(fwd_launch(ctx, S, T, 0, PV, trace_dev, k0, k1));
             launches++;
         }
     }
     HXC(cudaEventRecord(ctx->ev[1], ctx->st));
+    if (check_split(ctx)) return -1;
     ctx->launches[0] = launches;
     ctx->captured = capture;
     ctx->nstep = nstep;
@@ -652,23 +717,25 @@ static int run_backward(hx_ctx* ctx, const double* dLdv_dev) {
                    g + ctx->grad_off[HX_P_CM],        g + ctx->grad_off[HX_P_IC_AMP]};
     hx::DevProbe PV = hx_probe_view(ctx);
     hx::DevState S = state_view(ctx);
+    if (ctx->split) HXC(cudaMemsetAsync(ctx->split_err.p, 0, 4, ctx->st));
     HXC(cudaEventRecord(ctx->ev[2], ctx->st));
     int launches = 0;
     if (ctx->full_tape) {
         hx::DevTape T{ctx->tv.p, ctx->tm.p, ctx->th.p, ctx->tn.p, 0};
-        HXC(hx::launch_bwd(ctx->G, T, A, GR, PV, dLdv_dev, ctx->tmid.p, ctx->nstep, 0, ctx->st));
+        HXC(bwd_launch(ctx, T, A, GR, PV, dLdv_dev, ctx->nstep, 0));
         launches = 1;
     } else {
         for (int s = ctx->nseg - 1; s >= 0; s--) {
             int k0 = s * ctx->seg, k1 = std::min(ctx->nstep, k0 + ctx->seg);
             if (copy_ck(ctx, s, false)) return -1;
             hx::DevTape T{ctx->tv.p, ctx->tm.p, ctx->th.p, ctx->tn.p, k0};
-            HXC(hx::launch_fwd(ctx->G, S, T, 1, PV, nullptr, ctx->tmid.p, k0, k1, ctx->st));
-            HXC(hx::launch_bwd(ctx->G, T, A, GR, PV, dLdv_dev, ctx->tmid.p, k1, k0, ctx->st));
+            HXC(fwd_launch(ctx, S, T, 1, PV, nullptr, k0, k1));
+            HXC(bwd_launch(ctx, T, A, GR, PV, dLdv_dev, k1, k0));
             launches += 2;
         }
     }
     HXC(cudaEventRecord(ctx->ev[3], ctx->st));
+    if (check_split(ctx)) return -1;
     ctx->launches[1] = launches;
     return 0;
 }

@@ -1,0 +1,358 @@
+// hx_step.cuh -- device building blocks of the step kernels (shared by
+// hx_kernels.cu and hx_split.cu): the cell-group layout in shared memory, the
+// branch-level Hines solve and the per-node assembly of rhs/d.
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include "hx_dev.hpp"
+#include "hx_mech.cuh"
+
+namespace hx {
+
+// ------------------------------------------------------------------ Hines (shared memory)
+// hines_cell (below) solves one cell's tree system in place: d (diagonal in,
+// reciprocal of the eliminated diagonal out), rhs (right-hand side in, solution
+// out).  sa/sb are the axial coefficients in shared memory; A eliminates a
+// child into its parent and U couples a node to its parent (forward: A=a, U=b;
+// transposed system: A=b, U=a).
+//
+// The reference eliminates with a division on every step of the chain
+// (solve_serial, simulate.cpp:558-581).  Here the eliminated diagonal and rhs
+// of an unbranched chain are carried in projective form (tri_block below), so
+// the serial dependencies are FMAs only; exact power-of-two rescaling keeps
+// p, q, y in range and the reciprocals are formed off the chains with a
+// branch-free Newton reciprocal.  The back-substitution is one FMA per node.
+__device__ __forceinline__ double rescale_pow2(double x) {
+    // 2^-floor(log2 x) for positive normal x; exact
+    const long long e = ((__double_as_longlong(x) >> 52) & 0x7FF);
+    return __longlong_as_double((2046LL - e) << 52);
+}
+
+// Register-blocked chain kernels.  Every block loads up to kBlk nodes' operands
+// from shared memory into registers before the dependent arithmetic and stores
+// the results afterwards, so that no shared-memory load waits behind a store
+// of the same array on the critical path.  cnt <= kBlk nodes are processed;
+// callers pass kBlk for full blocks.
+constexpr int kBlk = 4;
+
+// tri_block: triangularisation of a chain from node j downwards in projective
+// form.  With d'_k = p_k/q_k and the eliminated rhs r'_k = y_k/q_k:
+//   p_{k-1} = d_{k-1} p_k - A_k U_k q_k,   q_{k-1} = p_k,
+//   y_{k-1} = rhs_{k-1} p_k - A_k y_k,
+// two FMA chains without division.  For k = j .. j-cnt+1 it stores
+// d[k] = 1/d'_k = q_k/p_k and rhs[k] = r'_k/d'_k = y_k/p_k (the reciprocal is
+// off both chains) and leaves (p, q, y) of node j-cnt.
+template <bool kGuard>
+__device__ __forceinline__ void tri_block(double* __restrict__ d, double* __restrict__ rhs,
+                                          const double* __restrict__ A, const double* __restrict__ U, int j, int cnt,
+                                          double& pp, double& qq, double& yy) {
+    double dl[kBlk], rl[kBlk], al[kBlk], cl[kBlk], pv[kBlk], qv[kBlk], yv[kBlk];
+#pragma unroll
+    for (int u = 0; u < kBlk; ++u) {
+        if (!kGuard || u < cnt) {
+            dl[u] = d[j - 1 - u];
+            rl[u] = rhs[j - 1 - u];
+            al[u] = A[j - u];
+            cl[u] = al[u] * U[j - u];
+        }
+    }
+#pragma unroll
+    for (int u = 0; u < kBlk; ++u) {
+        if (!kGuard || u < cnt) {
+            pv[u] = pp;
+            qv[u] = qq;
+            yv[u] = yy;
+            const double pn = __fma_rn(dl[u], pp, -(cl[u] * qq));
+            const double yn = __fma_rn(rl[u], pp, -(al[u] * yy));
+            qq = pp;
+            pp = pn;
+            yy = yn;
+        }
+    }
+#pragma unroll
+    for (int u = 0; u < kBlk; ++u) {
+        if (!kGuard || u < cnt) {
+            const double ip = rcp_pos(pv[u]);
+            d[j - u] = qv[u] * ip;
+            rhs[j - u] = yv[u] * ip;
+        }
+    }
+}
+
+// back_block: x_k = rhs'_k/d'_k - (U_k/d'_k) x_{k-1} for k = j .. j+cnt-1
+// (d holds 1/d'_k, rhs holds rhs'_k/d'_k); one FMA per node on the chain.
+template <bool kGuard>
+__device__ __forceinline__ void back_block(const double* __restrict__ d, double* __restrict__ rhs,
+                                           const double* __restrict__ U, int j, int cnt, double& x) {
+    double hl[kBlk], gl[kBlk];
+#pragma unroll
+    for (int u = 0; u < kBlk; ++u) {
+        if (!kGuard || u < cnt) {
+            hl[u] = U[j + u] * d[j + u];
+            gl[u] = rhs[j + u];
+        }
+    }
+#pragma unroll
+    for (int u = 0; u < kBlk; ++u) {
+        if (!kGuard || u < cnt) {
+            x = __fma_rn(-hl[u], x, gl[u]);
+            gl[u] = x;
+        }
+    }
+#pragma unroll
+    for (int u = 0; u < kBlk; ++u)
+        if (!kGuard || u < cnt) rhs[j + u] = gl[u];
+}
+
+// ------------------------------------------------------------------ cell groups
+// Shared-memory copies of the pack's topology and schedule (int tables).
+struct Meta {
+    int* par;   // node parent (pack-local), -1 for roots
+    int* flag;  // NodeFlag bits
+    int* cho;   // node child offsets into ch (size n+1)
+    int* ch;    // node children (pack-local), ascending reference index
+    int* bh;    // branch head / end / head's parent (pack-local nodes)
+    int* be;
+    int* bp;
+    int* bco;   // branch child offsets into bc (size nbr+1)
+    int* bc;    // child-branch heads, descending reference index
+    int* lvl;   // level tables of the pack's cells (pack-local branch ids)
+};
+
+// One cell and the warps of the CTA that own it.
+struct Grp {
+    int nb, n;       // pack-local first node, node count
+    int tl, nt;      // thread index inside the group, group size
+    int bar, nwarp;  // named barrier id (multi-warp groups)
+    int lvl, nlev;   // offset of the cell's level table in Meta::lvl, levels
+    int slot;        // global cell-slot index
+    __device__ __forceinline__ void sync() const {
+        if (nwarp == 1)
+            __syncwarp();
+        else
+            asm volatile("bar.sync %0, %1;" ::"r"(bar), "r"(nt) : "memory");
+    }
+};
+
+__device__ __forceinline__ size_t meta_ints(const DevGroup& G) {
+    return 3 * (size_t)G.smem_n + 1 + G.smem_nch + 4 * (size_t)G.smem_br + 1 + G.smem_bch + G.smem_lvl;
+}
+
+// Loads the pack's tables into shared memory (whole CTA), then returns the
+// calling thread's cell group; false for warps the pack leaves idle.
+__device__ __forceinline__ bool setup_pack(const DevGroup& G, int p, int* ibase, Meta& M, Grp& g) {
+    const int tid = threadIdx.x, nt = blockDim.x;
+    M.par = ibase;
+    M.flag = M.par + G.smem_n;
+    M.cho = M.flag + G.smem_n;
+    M.ch = M.cho + G.smem_n + 1;
+    M.bh = M.ch + G.smem_nch;
+    M.be = M.bh + G.smem_br;
+    M.bp = M.be + G.smem_br;
+    M.bco = M.bp + G.smem_br;
+    M.bc = M.bco + G.smem_br + 1;
+    M.lvl = M.bc + G.smem_bch;
+    const int pb = G.pack_node_off[p], pn = G.pack_node_off[p + 1] - pb;
+    const int nch0 = G.pack_nch_off[p], nch = G.pack_nch_off[p + 1] - nch0;
+    const int br0 = G.pack_br_off[p], nbr = G.pack_br_off[p + 1] - br0;
+    const int bc0 = G.pack_bch_off[p], nbc = G.pack_bch_off[p + 1] - bc0;
+    const int s0 = G.pack_slot_off[p], s1 = G.pack_slot_off[p + 1];
+    const int l0 = G.cs_lvl_off[s0], l1 = G.cs_lvl_off[s1 - 1] + G.cs_nlev[s1 - 1] + 1;
+    for (int i = tid; i < pn; i += nt) {
+        M.par[i] = G.node_parent[pb + i];
+        M.flag[i] = G.node_flags[pb + i];
+        M.cho[i] = G.node_child_off[pb + i] - nch0;
+    }
+    if (tid == 0) M.cho[pn] = nch;
+    for (int k = tid; k < nch; k += nt) M.ch[k] = G.node_child[nch0 + k];
+    for (int k = tid; k < nbr; k += nt) {
+        M.bh[k] = G.br_head[br0 + k];
+        M.be[k] = G.br_end[br0 + k];
+        M.bp[k] = G.br_parent[br0 + k];
+        M.bco[k] = G.br_child_off[br0 + k] - bc0;
+    }
+    if (tid == 0) M.bco[nbr] = nbc;
+    for (int k = tid; k < nbc; k += nt) M.bc[k] = G.br_child[bc0 + k];
+    for (int k = tid; k < l1 - l0; k += nt) M.lvl[k] = G.level_br_off[l0 + k];
+    __syncthreads();
+    const int w = tid >> 5;
+    for (int s = s0; s < s1; ++s) {
+        const int w0 = G.cs_warp0[s], nw = G.cs_nwarp[s];
+        if (w >= w0 && w < w0 + nw) {
+            g.nb = G.cs_node0[s];
+            g.n = G.cs_nnode[s];
+            g.tl = tid - 32 * w0;
+            g.nt = 32 * nw;
+            g.bar = G.cs_bar[s];
+            g.slot = s;
+            g.nwarp = nw;
+            g.lvl = G.cs_lvl_off[s] - l0;
+            g.nlev = G.cs_nlev[s];
+            return true;
+        }
+    }
+    return false;
+}
+
+template <bool kTransposed>
+__device__ __forceinline__ void hines_cell(const Meta& M, const Grp& g, const double* __restrict__ sa,
+                                           const double* __restrict__ sb, double* __restrict__ d,
+                                           double* __restrict__ rhs) {
+    const double* __restrict__ A = kTransposed ? sb : sa;
+    const double* __restrict__ U = kTransposed ? sa : sb;
+    const int* lo = M.lvl + g.lvl;
+    for (int L = g.nlev - 1; L >= 0; --L) {
+        const int b1 = lo[L + 1];
+        for (int br = lo[L] + g.tl; br < b1; br += g.nt) {
+            const int h = M.bh[br], e = M.be[br];
+            double de = d[e], re = rhs[e];
+            // child branches fold into the end node (d[c] = 1/d'_c, rhs[c] = r'_c/d'_c)
+            const int c1 = M.bco[br + 1];
+            for (int k = M.bco[br]; k < c1; ++k) {
+                const int c = M.bc[k];
+                de = __fma_rn(-(A[c] * U[c]), d[c], de);
+                re = __fma_rn(-A[c], rhs[c], re);
+            }
+            double pp = de, qq = 1.0, yy = re;
+            int j = e;
+            for (; j - h >= kBlk; j -= kBlk) {
+                tri_block<false>(d, rhs, A, U, j, kBlk, pp, qq, yy);
+                const double s = rescale_pow2(pp);
+                pp *= s;
+                qq *= s;
+                yy *= s;
+            }
+            if (j > h) tri_block<true>(d, rhs, A, U, j, j - h, pp, qq, yy);
+            const double ip = rcp_pos(pp);
+            d[h] = qq * ip;
+            rhs[h] = yy * ip;
+        }
+        g.sync();
+    }
+    for (int L = 0; L < g.nlev; ++L) {
+        const int b1 = lo[L + 1];
+        for (int br = lo[L] + g.tl; br < b1; br += g.nt) {
+            const int h = M.bh[br], e = M.be[br];
+            const int par = M.bp[br];
+            double x = rhs[h];
+            if (par >= 0) x = __fma_rn(-(U[h] * d[h]), rhs[par], x);
+            rhs[h] = x;
+            int j = h + 1;
+            for (; e - j + 1 >= kBlk; j += kBlk) back_block<false>(d, rhs, U, j, kBlk, x);
+            if (j <= e) back_block<true>(d, rhs, U, j, e - j + 1, x);
+        }
+        g.sync();
+    }
+}
+
+// ------------------------------------------------------------------ assembly
+// One point-process contribution through MechTemp::current
+// (mech_template.cuh:612-645): i1 = I(v+0.001), i0 = I(v), scaled by 1e2/area.
+__device__ __forceinline__ void pp_add(double i1, double i0, double area, bool electrode, double& r, double& dd) {
+    double gg = (i1 - i0) * kInvFdEps;
+    gg *= 1.e2 / area;
+    i0 *= 1.e2 / area;
+    if (electrode) {
+        r += i0;
+        dd -= gg;
+    } else {
+        r -= i0;
+        dd += gg;
+    }
+}
+
+// Network currents of GPU node gi after IClamp, in the exported mechanism
+// order: ExpSyn, Exp2Syn (expsyn.cpp:92-121, exp2syn_temp.cuh:45-49), HalfGap
+// (HalfGap.cu:56-62, electrode), gapjunction_lr (gapjunction_lr.cu:58-65),
+// neuron_to_neuron_syn_lr (neuron_to_neuron_syn_lr.cu:120-127).  synA/synB are
+// the cell's synapse states indexed from syn0; grs the graded states s_k.
+__device__ __forceinline__ void assemble_net(const DevGroup& G, const DevNet& N, int gi, double vi,
+                                             const double* __restrict__ synA, const double* __restrict__ synB,
+                                             int syn0, const double* __restrict__ grs,
+                                             const double* __restrict__ vpeer, double& r, double& dd) {
+    const double area = __ldg(G.area + gi);
+    const int s1 = __ldg(N.node_syn_off + gi + 1);
+    for (int j = __ldg(N.node_syn_off + gi); j < s1; ++j) {
+        const double gs = synB[j - syn0] - synA[j - syn0], e = __ldg(N.syn_e + j);
+        pp_add(gs * ((vi + kFdEps) - e), gs * (vi - e), area, false, r, dd);
+    }
+    if (!N.coupled) return;
+    const int h1 = __ldg(N.node_hg_off + gi + 1);
+    for (int j = __ldg(N.node_hg_off + gi); j < h1; ++j) {
+        const double vg = vpeer[__ldg(N.hg_src + j)], g = __ldg(N.hg_g + j);
+        pp_add((vg - (vi + kFdEps)) * g, (vg - vi) * g, area, true, r, dd);
+    }
+    const int j1 = __ldg(N.node_gj_off + gi + 1);
+    for (int j = __ldg(N.node_gj_off + gi); j < j1; ++j) {
+        const double vp = vpeer[__ldg(N.gj_pre + j)], g = __ldg(N.gj_g + j), w = __ldg(N.gj_w + j);
+        pp_add(w * (g * ((vi + kFdEps) - vp)), w * (g * (vi - vp)), area, false, r, dd);
+    }
+    const int r1 = __ldg(N.node_gr_off + gi + 1);
+    for (int j = __ldg(N.node_gr_off + gi); j < r1; ++j) {
+        const double aw = fabs(__ldg(N.gr_w + j)), gs = __ldg(N.gr_g + j) * grs[j], er = __ldg(N.gr_erev + j);
+        pp_add(aw * (gs * ((vi + kFdEps) - er)), aw * (gs * (vi - er)), area, false, r, dd);
+    }
+}
+
+// rhs/d of pack-local node i in the reference's accumulation order:
+// pas, hh, IClamp (CoreNEURON type order), [network currents], capacitance
+// jacobian, axial terms.
+template <bool kRhs, bool kNet = false, bool kSplitAxial = false>
+__device__ __forceinline__ void assemble(const DevGroup& G, const Meta& M, int pb, int i, int fl,
+                                         const double* __restrict__ sv, const double* __restrict__ sa,
+                                         const double* __restrict__ sb, double m, double h, double n, double tmid,
+                                         double& r_out, double& d_out, const DevNet& N = DevNet{},
+                                         const double* synA = nullptr, const double* synB = nullptr, int syn0 = 0,
+                                         const double* grs = nullptr, const double* vpeer = nullptr) {
+    const int gi = pb + i;
+    const double vi = sv[i];
+    double r = 0.0, dd = 0.0;
+    if (fl & kHasPas) {  // pas_templated.cu:27-31 through MechTemp::current (FD conductance)
+        const double g = __ldg(G.pas_g + gi), e = __ldg(G.pas_e + gi);
+        double g1 = g * ((vi + kFdEps) - e);
+        const double i0 = g * (vi - e);
+        g1 = (g1 - i0) * kInvFdEps;
+        r -= i0;
+        dd += g1;
+    }
+    if (fl & kHasHH) {  // hh_templated.cu:137-149
+        const double gnabar = __ldg(G.hh_gnabar + gi), gkbar = __ldg(G.hh_gkbar + gi), gl = __ldg(G.hh_gl + gi);
+        const double ena = __ldg(G.hh_ena + gi), ek = __ldg(G.hh_ek + gi), el = __ldg(G.hh_el + gi);
+        double g1 = hh_current(vi + kFdEps, gnabar, gkbar, gl, m, h, n, ena, ek, el);
+        const double i0 = hh_current(vi, gnabar, gkbar, gl, m, h, n, ena, ek, el);
+        g1 = (g1 - i0) * kInvFdEps;
+        r -= i0;
+        dd += g1;
+    }
+    const int ic1 = __ldg(G.node_ic_off + gi + 1);
+    for (int k = __ldg(G.node_ic_off + gi); k < ic1; ++k) {  // iclamp_templated.cu:35-45, electrode
+        const int j = __ldg(G.node_ic + k);
+        const double del = __ldg(G.ic_del + j), dur = __ldg(G.ic_dur + j);
+        const double cur = (tmid < del + dur && tmid >= del) ? __ldg(G.ic_amp + j) : 0.0;
+        r += cur * (1.e2 / __ldg(G.area + gi));
+    }
+    if (kNet) assemble_net(G, N, gi, vi, synA, synB, syn0, grs, vpeer, r, dd);
+    dd += G.cfac * __ldg(G.cm + gi);
+    if (kSplitAxial) {  // parent / children may sit in other CTAs (a split cell)
+        r_out = r;
+        d_out = dd;
+        return;
+    }
+    const int par = M.par[i];
+    if (par >= 0) {
+        if (kRhs) r -= sb[i] * (sv[par] - vi);
+        dd -= sb[i];
+    }
+    const int c1 = M.cho[i + 1];
+    for (int k = M.cho[i]; k < c1; ++k) {
+        const int c = M.ch[k];
+        const double ac = sa[c];
+        if (kRhs) r += ac * (vi - sv[c]);
+        dd -= ac;
+    }
+    r_out = r;
+    d_out = dd;
+}
+
+}  // namespace hx

@@ -114,6 +114,7 @@ typedef struct hx_plan_stats {
     int nbranch;          /* branches over all packs */
     double imbalance;     /* max pack nodes / mean pack nodes */
     size_t smem_fwd, smem_bwd; /* dynamic shared memory per CTA (bytes) */
+    int nsub;             /* subtrees of a cell split across CTAs (0: no split) */
 } hx_plan_stats;
 
 /* ---- context ------------------------------------------------------------ */
@@ -148,6 +149,11 @@ int hx_get_plan_stats(hx_ctx* ctx, hx_plan_stats* out);
  * division-free form the kernels use. */
 int hx_plan_check(const hx_group_desc* desc, int nodes_per_warp, hx_plan_stats* out, double* max_abs_diff,
                   double* pq_rel_diff);
+/* The same with a per-CTA node capacity (0 = unlimited): a group of one cell
+ * larger than the capacity is split into a top part and subtrees, one CTA
+ * each, as hx_load_group does when a cell exceeds a CTA's shared memory. */
+int hx_plan_check_cap(const hx_group_desc* desc, int nodes_per_warp, int max_pack_nodes, hx_plan_stats* out,
+                      double* max_abs_diff, double* pq_rel_diff);
 
 /* Parameter access in reference instance order (replaces the handle-based
  * Sim.set/get_variable path, src/python_api/PyBindings.cpp:80-81). */
