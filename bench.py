@@ -7,11 +7,23 @@ against a teacher trace (conductances perturbed lognormally, sigma 0.2) and the
 reverse sweep producing every per-compartment conductance gradient.  The
 metric is forward+backward compartment-timesteps per second.
 
-  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--config 2|3|4|5]
 
 Multi-GPU runs are launched by torchrun, one process per GPU; every rank
 integrates its own 1024-cell batch (cells are independent: weak scaling, no
 data-path collective) and the time is the max over ranks.
+
+The other configurations of the same metric (not the headline line):
+  --config 3   one 50,000-compartment cell (<= 40 branch levels), 2000 steps,
+               split across CTAs (cooperative launch), gradients of every
+               segment's conductances;
+  --config 4   event network: --ncell cells per GPU (default 10,000) of the
+               config-2 recipe, 100 Exp2Syn each plus one NetStim (5 Hz,
+               noise 1) per cell, 8000 steps; on N GPUs the network has
+               N x ncell cells, sharded by cell, spikes all-gathered over NCCL
+               once per minimum-delay window (weak scaling);
+  --config 5   302 cells coupled by 900 HalfGap pairs and 2000 graded
+               synapses, 8000 steps (one step per launch).
 """
 from __future__ import annotations
 
@@ -55,7 +67,10 @@ def _alg_bytes(g):
     s = 1 + 3 * hh
     fwd = 8 * (p + 2 * s) + 4
     tot = 8 * (3 * p + 8 * s) + 12
-    return float(fwd.sum()), float((tot - fwd).sum()), float(tot.sum())
+    # event synapses: 2 states, 2 parameters each (188 B per instance-step)
+    nsyn = g.expsyn.n + g.exp2syn.n
+    syn_fwd, syn_tot = nsyn * (8 * (2 + 2 * 2) + 4), nsyn * (8 * (3 * 2 + 8 * 2) + 12)
+    return (float(fwd.sum()) + syn_fwd, float((tot - fwd).sum()) + syn_tot - syn_fwd, float(tot.sum()) + syn_tot)
 
 
 def _peaks():
@@ -239,37 +254,47 @@ def run_ours(args):
     torch.cuda.set_stream(stream)
 
     # ---- synthetic workload (per rank: its own cells)
-    seed0 = SEED0 + 100000 * rank
-    g = synth.random_tree_batch(args.ncell, seed0=seed0)
-    teacher = synth.perturb_conductances(g, 0.2, seed=seed0 + 7)
-    T = args.nstep
+    W = build_workload(args, ws, rank)
+    g, teacher, T, keys = W["group"], W["teacher"], W["nstep"], W["keys"]
+    probes = W["probes"]
     ncomp = g.nnode
-    keys = ("hh.gnabar", "hh.gkbar", "hh.gl", "pas.g")
 
-    tsim = Sim(local)
-    tsim.load_group(teacher)
-    target_h = tsim.simulate(T)
+    def new_sim(grp):
+        sim = Sim(local)
+        sim.set_stream(stream.cuda_stream)
+        sim.load_group(grp, gid_base=W.get("gid_base", 0), nsrc_cells=W.get("nsrc_cells", 0))
+        if ws > 1 and W.get("exchange"):
+            from heliox_b200 import shard
+
+            sim.set_window(W["window"])
+            sim.set_exchange(shard.allgather_exchange(), ws, W["exchange_cap"])
+        return sim
+
+    tsim = new_sim(teacher)
+    target_h = tsim.simulate(T, probes=probes)
+    torch.cuda.synchronize()
+    if ws > 1 and W.get("exchange"):
+        tsim.set_exchange(None, 1)
     tsim.close()
     del tsim
 
-    s = Sim(local)
-    s.set_stream(stream.cuda_stream)
-    s.load_group(g)
+    s = new_sim(g)
     target = torch.from_numpy(target_h).to(dev)
     trace = torch.empty_like(target)
     dLdv = torch.empty_like(target)
     loss = torch.zeros(1, dtype=torch.float64, device=dev)
-    counts = {"hh.gnabar": g.hh.n, "hh.gkbar": g.hh.n, "hh.gl": g.hh.n, "pas.g": g.pas.n}
-    grads = {k: torch.empty(n, dtype=torch.float64, device=dev) for k, n in counts.items()}
+    counts = {k: s._count(k) for k in keys}
+    grads = {k: torch.empty(max(n, 1), dtype=torch.float64, device=dev) for k, n in counts.items()}
+    nprobe = int(probes.shape[0])
     flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=dev)  # > L2 (126 MB)
 
     def step(ev=None):
         if ev is not None:
             ev[0].record(stream)
-        s.forward_capture_dev(T, trace.data_ptr())
+        s.forward_capture_dev(T, trace.data_ptr(), probes=probes)
         if ev is not None:
             ev[1].record(stream)
-        s.mse_loss_grad_dev(trace.data_ptr(), target.data_ptr(), T + 1, g.ncell, dLdv.data_ptr(), loss.data_ptr())
+        s.mse_loss_grad_dev(trace.data_ptr(), target.data_ptr(), T + 1, nprobe, dLdv.data_ptr(), loss.data_ptr())
         if ev is not None:
             ev[2].record(stream)
         s.backward_dev(dLdv.data_ptr(), {k: v.data_ptr() for k, v in grads.items()})
@@ -309,27 +334,33 @@ def run_ours(args):
     fwd_ms = statistics.mean(e[0].elapsed_time(e[1]) for e in evs)
     bwd_ms = statistics.mean(e[2].elapsed_time(e[3]) for e in evs)
     loss_val = float(loss.item())
-    # launches of our kernels per step: init, forward, MSE (2), backward, 4 gradient gathers
-    gpu_launches = args.steps * (1 + 1 + 2 + 1 + len(keys))
+    # launches of our kernels per step, as the runtime counts them (forward
+    # and backward kernels, incl. windows / checkpoint replays / per-step
+    # launches of coupled groups) plus init, MSE (2) and the gradient gathers
+    _, nf = s.last_kernel_ms(0)
+    _, nb = s.last_kernel_ms(1)
+    gpu_launches = args.steps * (1 + nf + 2 + nb + len(keys))
 
     # ---- end to end through the public host-buffer API (params in, loss/grads out)
     host_params = {k: np.ascontiguousarray(s.get_param_array(k)) for k in keys}
-    s.set_stream(0)
+    if not (ws > 1 and W.get("exchange")):  # the exchange hook runs on torch's stream
+        s.set_stream(0)
     torch.cuda.synchronize()
-    h2d = sum(v.nbytes for v in host_params.values()) + (T + 1) * g.ncell * 8
-    d2h = (T + 1) * g.ncell * 8 + sum(8 * counts[k] for k in keys)
+    h2d = sum(v.nbytes for v in host_params.values()) + (T + 1) * nprobe * 8
+    d2h = (T + 1) * nprobe * 8 + sum(8 * counts[k] for k in keys)
     if dist:
         dist.barrier()
+    e2e_steps = args.steps if args.config == 2 else 1
     t0 = time.perf_counter()
-    for _ in range(args.steps):
+    for _ in range(e2e_steps):
         for k in keys:
             s.set_param_array(k, host_params[k])
-        tr = s.forward_capture(T)
+        tr = s.forward_capture(T, probes=probes)
         err = tr - target_h
-        dl = (2.0 / (T * g.ncell)) * err
+        dl = (2.0 / (T * nprobe)) * err
         dl[0] = 0.0
         gg = s.backward(dl, keys=keys)
-    e2e_s = time.perf_counter() - t0
+    e2e_s = (time.perf_counter() - t0) * args.steps / e2e_steps
     if dist:
         dist.barrier()
 
@@ -366,11 +397,10 @@ def run_ours(args):
             "dtype": "f64",
             "data": "synthetic",
             "config": {
-                "workload": f"config2: {args.ncell} seeded random-tree cells per GPU (hh+pas, IClamp), "
-                            f"{T} steps dt 0.025 ms, soma-MSE vs lognormal teacher, forward + exact adjoint",
+                "workload": W["workload"],
                 "compartments_per_gpu": ncomp,
-                "parallelism": f"cells sharded, {ws} GPU(s), no collective on the data path",
-                "l2": "tape (32 B/compartment-step, ~78 GB) exceeds L2; 256 MiB flush write between steps",
+                "parallelism": W["parallelism"].format(ws=ws),
+                "l2": "tape exceeds L2; 256 MiB flush write between steps",
                 "loss": loss_val,
             },
             "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h)},
@@ -385,14 +415,15 @@ def run_ours(args):
                 "peak_source": peak_src,
                 "unit": "GB/s",
                 "frac": achieved / peak,
-                "traffic": BWD_DRAM_BYTES_PER_UNIT * units_per_step / ws if BWD_DRAM_BYTES_PER_UNIT else None,
+                "traffic": (BWD_DRAM_BYTES_PER_UNIT * units_per_step / ws
+                            if BWD_DRAM_BYTES_PER_UNIT and args.config == 2 else None),
                 "alg_bytes_per_launch": bb * T,
                 "fwd_frac": (fb * T / (fwd_ms / 1e3) / 1e9) / peak,
                 "path_frac": (tb * T / ((fwd_ms + bwd_ms) / 1e3) / 1e9) / peak,
             },
             "clocks": clocks,
         }
-        if ws == 1 and not args.no_cpu:
+        if ws == 1 and not args.no_cpu and args.config == 2:
             procs = os.cpu_count() or 1
             ns = 4 * max(procs, 8)
             v, units, wall, kind = cpu_baseline(ns, T, procs)
@@ -401,10 +432,66 @@ def run_ours(args):
                                     "sample": f"{ns} cells of the config-2 batch, {T} steps; forward: {fwd_by}, "
                                               f"adjoint: oracle port; {wall:.1f} s per core"}
         print(json.dumps(line), flush=True)
+    if ws > 1 and W.get("exchange"):
+        s.set_exchange(None, 1)
     s.close()
     if dist:
         dist.destroy_process_group()
     return 0
+
+
+def build_workload(args, ws, rank):
+    """The synthetic group of one rank, its teacher, probes and trained parameters."""
+    import numpy as np
+
+    from heliox_b200 import shard, synth
+
+    if args.config == 2:
+        seed0 = SEED0 + 100000 * rank
+        g = synth.random_tree_batch(args.ncell, seed0=seed0)
+        return {"group": g, "teacher": synth.perturb_conductances(g, 0.2, seed=seed0 + 7), "nstep": args.nstep,
+                "keys": ("hh.gnabar", "hh.gkbar", "hh.gl", "pas.g"), "probes": g.soma_nodes(),
+                "workload": f"config2: {args.ncell} seeded random-tree cells per GPU (hh+pas, IClamp), "
+                            f"{args.nstep} steps dt 0.025 ms, soma-MSE vs lognormal teacher, forward + exact adjoint",
+                "parallelism": "cells sharded, {ws} GPU(s), no collective on the data path"}
+    if args.config == 3:
+        g = synth.giant_cell()
+        probes = np.unique(np.linspace(0, g.nnode - 1, 64).astype(np.int32))
+        T = 2000 if args.nstep == T_STEPS else args.nstep
+        return {"group": g, "teacher": synth.perturb_conductances(g, 0.2, seed=SEED0 + 3), "nstep": T,
+                "keys": ("hh.gnabar", "hh.gkbar", "hh.gl", "pas.g"), "probes": probes,
+                "workload": f"config3: one {g.nnode}-compartment random tree ({g.meta.get('levels')} branch levels), "
+                            f"{T} steps, MSE at 64 probes vs lognormal teacher, gradients of every segment's "
+                            "conductances; split across CTAs (cooperative launch)",
+                "parallelism": "replicas: one cell per GPU ({ws} GPU(s))"}
+    if args.config == 4:
+        ncell = args.ncell if args.ncell != NCELL else 10000
+        T = 8000 if args.nstep == T_STEPS else args.nstep
+        g = synth.network_config4_shard(ncell, rank, ws)
+        teacher = g.copy()
+        rng = np.random.default_rng(SEED0 + 4)
+        teacher.exp2syn.fields["weight"] = teacher.exp2syn.fields["weight"] * np.exp(
+            0.2 * rng.standard_normal(teacher.exp2syn.n))
+        W = shard.window_of(g)
+        return {"group": g, "teacher": teacher, "nstep": T, "keys": ("Exp2Syn.weight", "hh.gnabar"),
+                "probes": g.soma_nodes(), "gid_base": rank * ncell, "nsrc_cells": ws * ncell, "exchange": ws > 1,
+                "window": W, "exchange_cap": ncell * ((W + 1) // 2) + 1,
+                "workload": f"config4: event network, {ncell} cells per GPU x 100 Exp2Syn + 1 NetStim (5 Hz) "
+                            f"each, {T} steps, soma MSE vs teacher (weights perturbed), weight gradients",
+                "parallelism": "cells sharded over {ws} GPU(s); window spike all-gather over NCCL"}
+    if args.config == 5:
+        g = synth.worm_config5()
+        teacher = g.copy()
+        rng = np.random.default_rng(SEED0 + 5)
+        teacher.halfgap.fields["g"] = teacher.halfgap.fields["g"] * np.exp(0.2 * rng.standard_normal(g.halfgap.n))
+        teacher.graded.fields["w"] = teacher.graded.fields["w"] * np.exp(0.2 * rng.standard_normal(g.graded.n))
+        T = 8000 if args.nstep == T_STEPS else args.nstep
+        return {"group": g, "teacher": teacher, "nstep": T,
+                "keys": ("HalfGap.g", "neuron_to_neuron_syn_lr.w", "hh.gnabar"), "probes": g.soma_nodes(),
+                "workload": f"config5: {g.ncell} cells, {g.halfgap.n // 2} HalfGap pairs, {g.graded.n} graded "
+                            f"synapses, {T} steps, soma MSE vs teacher, gap and synapse gradients",
+                "parallelism": "replicas only ({ws} GPU(s)): coupled every step"}
+    raise ValueError(f"unknown config {args.config}")
 
 
 def main():
@@ -416,6 +503,7 @@ def main():
     ap.add_argument("--ncell", type=int, default=NCELL)
     ap.add_argument("--nstep", type=int, default=T_STEPS)
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU-baseline leg")
+    ap.add_argument("--config", type=int, default=2, choices=(2, 3, 4, 5))
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

@@ -314,9 +314,25 @@ def network_config4(ncell: int = 10000, seed: int = 4, syn_per_cell: int = 100, 
     NetStim per cell (``rate_hz``, noise 1, start 0, unlimited number) drives
     one more Exp2Syn at the soma.  Seeded; the reference quotes no data set.
     """
-    rng = np.random.default_rng(seed)
-    cells = [random_tree_cell(seed * 100000 + c, nmin=nmin, nmax=nmax) for c in range(ncell)]
-    g = concat_groups(cells, name=f"net{ncell}")
+    return network_config4_shard(ncell, 0, 1, seed=seed, syn_per_cell=syn_per_cell, nmin=nmin, nmax=nmax,
+                                 rate_hz=rate_hz)
+
+
+def network_config4_shard(ncell: int, rank: int, nranks: int, seed: int = 4, syn_per_cell: int = 100,
+                          nmin: int = 400, nmax: int = 600, rate_hz: float = 5.0) -> CellGroup:
+    """Rank ``rank``'s part of a config-4 network of ``nranks * ncell`` cells.
+
+    Built directly per rank (no rank needs the others' cells): cells
+    ``rank*ncell .. (rank+1)*ncell - 1`` seeded by their global id, their
+    synapses with global NetCon sources drawn over all cells, and the whole
+    NetStim table (one per global cell).  ``meta`` records ``gid_base`` and
+    ``nsrc_cells`` for ``Sim.load_group``.
+    """
+    total = ncell * nranks
+    base = rank * ncell
+    cells = [random_tree_cell(seed * 100000 + base + c, nmin=nmin, nmax=nmax) for c in range(ncell)]
+    g = concat_groups(cells, name=f"net{total}.r{rank}")
+    rng = np.random.default_rng([seed, rank])
     cell = g.cell_of_node()
     order = np.argsort(cell, kind="stable")
     bounds = np.searchsorted(cell[order], np.arange(ncell + 1))
@@ -324,23 +340,26 @@ def network_config4(ncell: int = 10000, seed: int = 4, syn_per_cell: int = 100, 
     post = np.repeat(np.arange(ncell), syn_per_cell)
     pick = bounds[post] + (rng.random(nsyn) * (bounds[post + 1] - bounds[post])).astype(np.int64)
     nodes = order[pick]
-    src = rng.integers(0, ncell - 1, nsyn)
-    src = np.where(src >= post, src + 1, src)
+    src = rng.integers(0, total - 1, nsyn)
+    src = np.where(src >= post + base, src + 1, src)  # no self-connection
     exc = rng.random(nsyn) < 0.8
     e = np.where(exc, 0.0, -80.0)
     d = rng.uniform(1.0, 5.0, nsyn)
     w = np.exp(rng.normal(-7.0, 1.0, nsyn))
+    # the NetStim of every local cell drives one more synapse at its soma
     nodes = np.concatenate([nodes, np.arange(ncell)])
-    src = np.concatenate([src, ncell + np.arange(ncell)])
+    src = np.concatenate([src, total + base + np.arange(ncell)])
     e = np.concatenate([e, np.zeros(ncell)])
     d = np.concatenate([d, rng.uniform(1.0, 5.0, ncell)])
     w = np.concatenate([w, np.full(ncell, 0.01)])
     n = nodes.shape[0]
     g.exp2syn = _table(nodes, {"tau1": np.full(n, 0.5), "tau2": np.full(n, 5.0), "e": e, "delay": d, "weight": w},
                        {"src": src})
-    g.netstim = MechTable(_i32(np.zeros(ncell)), {
-        "interval": _f64(np.full(ncell, 1000.0 / rate_hz)), "number": _f64(np.full(ncell, 1e9)),
-        "start": _f64(np.zeros(ncell)), "noise": _f64(np.ones(ncell))})
+    g.netstim = MechTable(_i32(np.zeros(total)), {
+        "interval": _f64(np.full(total, 1000.0 / rate_hz)), "number": _f64(np.full(total, 1e9)),
+        "start": _f64(np.zeros(total)), "noise": _f64(np.ones(total))})
+    g.meta["gid_base"] = base
+    g.meta["nsrc_cells"] = total
     g.validate()
     return g
 
