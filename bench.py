@@ -45,9 +45,9 @@ T_STEPS = 4000
 NCELL = 1024
 SEED0 = 20240
 # DRAM bytes per compartment-step of the backward kernel from the committed ncu
-# capture (profiles/fwd_bwd_kernels_trees296.md: dram__bytes_read.sum +
+# capture (profiles/fwd_bwd_kernels_config2_small.md: dram__bytes_read.sum +
 # dram__bytes_write.sum over the captured launch / its compartment-steps).
-BWD_DRAM_BYTES_PER_UNIT = 34.7
+BWD_DRAM_BYTES_PER_UNIT = 34.6
 
 
 def _alg_bytes(g):
