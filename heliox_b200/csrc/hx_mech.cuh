@@ -4,10 +4,16 @@
 // cnexp update written without its redundant divisions: the reference's
 //   m += (1 - exp(dt*(-1/mtau))) * ((minf/mtau)/(1/mtau) - m),  mtau = 1/(q10*(a+b))
 // is computed as
-//   m += (1 - exp(-dt*q10*(a+b))) * (minf - m),
-// and divisions by the constants 10, 18, 20, 80 are multiplications by their
-// reciprocals.  These forms equal the reference's mathematically and differ by
-// rounding only (parity is checked against the reference-order CPU oracle).
+//   m += (1 - exp(-dt*q10*(a+b))) * (minf - m).
+// The six exponentials of the rate functions all have arguments linear in v
+// with slopes 1/10, 1/18, 1/20, 1/80, so they are integer powers of one
+// exponential z = exp(-(v+65)/720) times constants:
+//   exp(-(v+65)/18) = z^40, exp(-(v+65)/20) = z^36, exp(-(v+65)/80) = z^9,
+//   exp(-(v+40)/10) = z^72 e^2.5, exp(-(v+55)/10) = z^72 e, exp(-(v+35)/10) = z^72 e^3,
+// and quotients by positive sums use a Newton reciprocal.  These forms equal
+// the reference's mathematically and differ by rounding only (a few 1e-14
+// relative in the rates); parity is checked against the reference-order CPU
+// oracle.
 // The finite-difference conductance of MechTemp::current
 // (mech_template.cuh:615-626) is kept: it is what the reference integrates.
 #pragma once
@@ -32,89 +38,109 @@ __device__ __forceinline__ double rcp_pos(double x) {
     return r;
 }
 
-// vtrap(x, 10) of hh_templated.cu:76-85 and its derivative in x.
-__device__ __forceinline__ double vtrap10(double x) {
-    const double u = x * 0.1;
-    if (fabs(u) < 1e-6) return 10.0 * (1 - u * 0.5);
-    return x / (exp(u) - 1);
-}
-
-__device__ __forceinline__ void vtrap10_d(double x, double& f, double& df) {
-    const double u = x * 0.1;
-    if (fabs(u) < 1e-6) {
-        f = 10.0 * (1 - u * 0.5);
-        df = -0.5;
-    } else {
-        const double e = exp(u);
-        const double em1 = e - 1;
-        const double r = 1.0 / em1;
-        f = x * r;
-        df = (em1 - u * e) * (r * r);
-    }
-}
-
 // Steady states and rate sums (k = q10*(alpha+beta) = 1/tau) of m, h, n.
 struct HHRates {
     double inf[3], k[3];
 };
 
+// e^2.5, e^3, e: the offsets of the vtrap / beta_h exponentials against z^72
+constexpr double kE25 = 12.182493960703473;
+constexpr double kE3 = 20.085536923187668;
+constexpr double kE1 = 2.718281828459045;
+
+// powers of z = exp(-(v+65)/720) used by the rates
+struct ZPow {
+    double z9, z36, z40, z72;
+};
+
+__device__ __forceinline__ ZPow zpow(double v) {
+    const double z = exp(-(v + 65.0) * (1.0 / 720.0));
+    const double z2 = z * z, z4 = z2 * z2, z8 = z4 * z4, z9 = z8 * z;
+    const double z18 = z9 * z9, z36 = z18 * z18;
+    return ZPow{z9, z36, z36 * z4, z36 * z36};
+}
+
+// vtrap(x, 10) = x / (exp(x/10) - 1) with exp(x/10) given; the reference's
+// small-argument branch (hh_templated.cu:76-85) is kept
+__device__ __forceinline__ double vtrap10_e(double x, double ex) {
+    const double u = x * 0.1;
+    if (fabs(u) < 1e-6) return 10.0 * (1 - u * 0.5);
+    return x / (ex - 1);
+}
+
 __device__ __forceinline__ void hh_rates(double v, double q10, HHRates& r) {
+    const ZPow Z = zpow(v);
     double al, be, s;
-    al = 0.1 * vtrap10(-(v + 40));
-    be = 4 * exp(-(v + 65) * (1.0 / 18));
+    al = 0.1 * vtrap10_e(-(v + 40), Z.z72 * kE25);
+    be = 4 * Z.z40;
     s = al + be;
-    r.inf[0] = al / s;
+    r.inf[0] = al * rcp_pos(s);
     r.k[0] = q10 * s;
-    al = 0.07 * exp(-(v + 65) * (1.0 / 20));
-    be = 1.0 / (exp(-(v + 35) * 0.1) + 1);
+    al = 0.07 * Z.z36;
+    be = rcp_pos(Z.z72 * kE3 + 1);
     s = al + be;
-    r.inf[1] = al / s;
+    r.inf[1] = al * rcp_pos(s);
     r.k[1] = q10 * s;
-    al = 0.01 * vtrap10(-(v + 55));
-    be = 0.125 * exp(-(v + 65) * (1.0 / 80));
+    al = 0.01 * vtrap10_e(-(v + 55), Z.z72 * kE1);
+    be = 0.125 * Z.z9;
     s = al + be;
-    r.inf[2] = al / s;
+    r.inf[2] = al * rcp_pos(s);
     r.k[2] = q10 * s;
 }
 
-// Rates plus d inf/dv and d(alpha+beta)/dv (shared exponentials).
+// vtrap10 and its derivative in x, exp(x/10) given
+__device__ __forceinline__ void vtrap10_d_e(double x, double ex, double& f, double& df) {
+    const double u = x * 0.1;
+    if (fabs(u) < 1e-6) {
+        f = 10.0 * (1 - u * 0.5);
+        df = -0.5;
+    } else {
+        const double em1 = ex - 1;
+        const double r = 1.0 / em1;
+        f = x * r;
+        df = (em1 - u * ex) * (r * r);
+    }
+}
+
+// Rates plus d inf/dv and d(alpha+beta)/dv.
 struct HHRatesD {
     double inf[3], k[3], dinf[3], ds[3];
 };
 
 __device__ __forceinline__ void hh_rates_d(double v, double q10, HHRatesD& r) {
+    const ZPow Z = zpow(v);
     double al, be, dal, dbe, s, f, df, rs;
-    vtrap10_d(-(v + 40), f, df);
+    vtrap10_d_e(-(v + 40), Z.z72 * kE25, f, df);
     al = 0.1 * f;
     dal = -0.1 * df;
-    be = 4 * exp(-(v + 65) * (1.0 / 18));
+    be = 4 * Z.z40;
     dbe = be * (-1.0 / 18);
     s = al + be;
-    rs = 1.0 / s;
+    rs = rcp_pos(s);
     r.inf[0] = al * rs;
     r.k[0] = q10 * s;
     r.dinf[0] = (dal * be - al * dbe) * (rs * rs);
     r.ds[0] = dal + dbe;
-    al = 0.07 * exp(-(v + 65) * (1.0 / 20));
+    al = 0.07 * Z.z36;
     dal = al * (-1.0 / 20);
     {
-        const double u = exp(-(v + 35) * 0.1);
-        be = 1.0 / (u + 1);
+        const double u = Z.z72 * kE3;
+        be = rcp_pos(u + 1);
         dbe = u * 0.1 * (be * be);
     }
     s = al + be;
-    rs = 1.0 / s;
+    rs = rcp_pos(s);
     r.inf[1] = al * rs;
     r.k[1] = q10 * s;
     r.dinf[1] = (dal * be - al * dbe) * (rs * rs);
     r.ds[1] = dal + dbe;
-    vtrap10_d(-(v + 55), f, df);
+    vtrap10_d_e(-(v + 55), Z.z72 * kE1, f, df);
     al = 0.01 * f;
     dal = -0.01 * df;
-    be = 0.125 * exp(-(v + 65) * (1.0 / 80));
+    be = 0.125 * Z.z9;
     dbe = be * (-1.0 / 80);
     s = al + be;
-    rs = 1.0 / s;
+    rs = rcp_pos(s);
     r.inf[2] = al * rs;
     r.k[2] = q10 * s;
     r.dinf[2] = (dal * be - al * dbe) * (rs * rs);
