@@ -154,6 +154,9 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_kernel(DevGroup G, DevState S
         const double tm = tmid[k];
         // A: assembly
         for (int i = i0 + g.tl; i < i1; i += g.nt) {
+            const int fl = M.flag[i];
+            NodePar q;
+            load_par(G, pb + i, fl, q);
             double r, dd;
             if (kNet) {
                 const int gi = pb + i;
@@ -172,10 +175,10 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_kernel(DevGroup G, DevState S
                         if (write_tape) N.tS[(size_t)(k - T.k_base + 1) * N.ngr + j] = sj;
                     }
                 }
-                assemble<true, true>(G, M, pb, i, M.flag[i], sv, sa, sb, sgm[i], sgh[i], sgn[i], tm, r, dd, N, ssA,
-                                     ssB, ps0, N.gr_s, N.vpeer);
+                assemble<true, true>(G, M, pb, i, fl, q, sv[i], sv, sa, sb, sgm[i], sgh[i], sgn[i], tm, r, dd, N,
+                                     ssA, ssB, ps0, N.gr_s, N.vpeer);
             } else {
-                assemble<true>(G, M, pb, i, M.flag[i], sv, sa, sb, sgm[i], sgh[i], sgn[i], tm, r, dd);
+                assemble<true>(G, M, pb, i, fl, q, sv[i], sv, sa, sb, sgm[i], sgh[i], sgn[i], tm, r, dd);
             }
             srhs[i] = r;
             sd[i] = dd;
@@ -339,6 +342,9 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_kernel(DevGroup G, DevTape T,
                 slh[i] = lam[1];
                 sln[i] = lam[2];
             }
+            // (parameters loaded after the rate chain: held across it they spill)
+            NodePar q;
+            load_par(G, pb + i, fl, q);
             double r, dd;
             if (kNet) {
                 const int s1 = __ldg(N.node_syn_off + pb + i + 1);
@@ -346,9 +352,10 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_kernel(DevGroup G, DevTape T,
                     slA[j - ps0] *= 1.0 - __ldg(N.syn_cA + j);
                     slB[j - ps0] *= 1.0 - __ldg(N.syn_cB + j);
                 }
-                assemble<false, true>(G, M, pb, i, fl, svk, sa, sb, gm, gh, gn, tm, r, dd, N, tA, tB, 0, grs, vpeer);
+                assemble<false, true>(G, M, pb, i, fl, q, svk[i], svk, sa, sb, gm, gh, gn, tm, r, dd, N, tA, tB, 0,
+                                      grs, vpeer);
             } else {
-                assemble<false>(G, M, pb, i, fl, svk, sa, sb, gm, gh, gn, tm, r, dd);
+                assemble<false>(G, M, pb, i, fl, q, svk[i], svk, sa, sb, gm, gh, gn, tm, r, dd);
             }
             sd[i] = dd;
             sw[i] = mu;
@@ -361,37 +368,18 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_kernel(DevGroup G, DevTape T,
         for (int i = i0 + g.tl; i < i1; i += g.nt) {
             const int gi = pb + i;
             const int fl = M.flag[i];
+            NodePar q;
+            load_par(G, gi, fl, q);
             const double w = sw[i];
             const double vk = svk[i];
             const double ld = -w * (svk1[i] - vk);
-            double lvn = slv[i];
-            if (fl & kHasPas) {
-                const double gp = __ldg(G.pas_g + gi);
-                GR.pas_g[gi] += ld - w * (vk - __ldg(G.pas_e + gi));
-                GR.pas_e[gi] += w * gp;
-                lvn -= w * gp;
-            }
+            const double lvn0 = slv[i];
+            double lm = slm[i], lh = slh[i], ln = sln[i];
+            double lvn = vjp_mech(G, GR, T, off, i, gi, fl, q, w, vk, ld, tm, lvn0, lm, lh, ln);
             if (fl & kHasHH) {
-                const double m = T.m[off + i], h = T.h[off + i], nn = T.n[off + i];
-                const double gnabar = __ldg(G.hh_gnabar + gi), gkbar = __ldg(G.hh_gkbar + gi), gl = __ldg(G.hh_gl + gi);
-                const double t_na = ld - w * (vk - __ldg(G.hh_ena + gi));
-                const double t_k = ld - w * (vk - __ldg(G.hh_ek + gi));
-                const double t_l = ld - w * (vk - __ldg(G.hh_el + gi));
-                const double m2h = m * m * h, n3 = nn * nn * nn;
-                GR.hh_gnabar[gi] += m2h * m * t_na;
-                GR.hh_gkbar[gi] += n3 * nn * t_k;
-                GR.hh_gl[gi] += t_l;
-                GR.hh_el[gi] += w * gl;
-                slm[i] += 3.0 * gnabar * m2h * t_na;
-                slh[i] += gnabar * m * m * m * t_na;
-                sln[i] += 4.0 * gkbar * n3 * t_k;
-                lvn -= w * (gnabar * m2h * m + gkbar * n3 * nn + gl);
-            }
-            const int ic1 = __ldg(G.node_ic_off + gi + 1);
-            for (int k2 = __ldg(G.node_ic_off + gi); k2 < ic1; ++k2) {
-                const int j = __ldg(G.node_ic + k2);
-                const double del = __ldg(G.ic_del + j), dur = __ldg(G.ic_dur + j);
-                if (tm < del + dur && tm >= del) GR.ic_amp[j] += w * (1.e2 / __ldg(G.area + gi));
+                slm[i] = lm;
+                slh[i] = lh;
+                sln[i] = ln;
             }
             if (kNet) {
                 const double sarea = 1.e2 / __ldg(G.area + gi);
@@ -407,9 +395,9 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_kernel(DevGroup G, DevTape T,
                 if (N.coupled) {
                     const int h1 = __ldg(N.node_hg_off + gi + 1);
                     for (int j = __ldg(N.node_hg_off + gi); j < h1; ++j) {
-                        const int q = __ldg(N.hg_src + j);
+                        const int src = __ldg(N.hg_src + j);
                         const double gg = __ldg(N.hg_g + j);
-                        GR.hg_g[j] += w * sarea * (vpeer[q] - vk) + ld * sarea;
+                        GR.hg_g[j] += w * sarea * (vpeer[src] - vk) + ld * sarea;
                         lvn -= w * sarea * gg;
                         N.x_hg_out[j] = w * sarea * gg;
                     }
@@ -450,7 +438,6 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_kernel(DevGroup G, DevTape T,
                     }
                 }
             }
-            GR.cm[gi] += ld * G.cfac;
             const int par = M.par[i];
             if (par >= 0) lvn += sb[i] * w - sa[i] * sw[par];
             const int c1n = M.cho[i + 1];

@@ -227,7 +227,10 @@ __global__ void __launch_bounds__(kThreads, 1) split_fwd_kernel(DevGroup G, DevS
         const double tm = tmid[k];
         for (int i = i0 + g.tl; i < i1; i += g.nt) {
             double r, dd;
-            assemble<true, false, true>(G, M, pb, i, M.flag[i], sv, sa, sb, sgm[i], sgh[i], sgn[i], tm, r, dd);
+            const int fl = M.flag[i];
+            NodePar q;
+            load_par(G, pb + i, fl, q);
+            assemble<true, false, true>(G, M, pb, i, fl, q, sv[i], sv, sa, sb, sgm[i], sgh[i], sgn[i], tm, r, dd);
             axial_split<true>(G, M, X, i, sv, sa, sb, r, dd);
             srhs[i] = r;
             sd[i] = dd;
@@ -384,8 +387,10 @@ __global__ void __launch_bounds__(kThreads, 1) split_bwd_kernel(DevGroup G, DevT
                 slh[i] = lam[1];
                 sln[i] = lam[2];
             }
+            NodePar q;
+            load_par(G, pb + i, fl, q);
             double r, dd;
-            assemble<false, false, true>(G, M, pb, i, fl, svk, sa, sb, gm, gh, gn, tm, r, dd);
+            assemble<false, false, true>(G, M, pb, i, fl, q, svk[i], svk, sa, sb, gm, gh, gn, tm, r, dd);
             axial_split<false>(G, M, X, i, svk, sa, sb, r, dd);
             sd[i] = dd;
             sw[i] = mu;
@@ -401,39 +406,18 @@ __global__ void __launch_bounds__(kThreads, 1) split_bwd_kernel(DevGroup G, DevT
         for (int i = i0 + g.tl; i < i1; i += g.nt) {
             const int gi = pb + i;
             const int fl = M.flag[i];
+            NodePar q;
+            load_par(G, gi, fl, q);
             const double w = sw[i];
             const double vk = svk[i];
             const double ld = -w * (svk1[i] - vk);
-            double lvn = slv[i];
-            if (fl & kHasPas) {
-                const double gp = __ldg(G.pas_g + gi);
-                GR.pas_g[gi] += ld - w * (vk - __ldg(G.pas_e + gi));
-                GR.pas_e[gi] += w * gp;
-                lvn -= w * gp;
-            }
+            double lm = slm[i], lh = slh[i], ln = sln[i];
+            double lvn = vjp_mech(G, GR, T, off, i, gi, fl, q, w, vk, ld, tm, slv[i], lm, lh, ln);
             if (fl & kHasHH) {
-                const double m = T.m[off + i], h = T.h[off + i], nn = T.n[off + i];
-                const double gnabar = __ldg(G.hh_gnabar + gi), gkbar = __ldg(G.hh_gkbar + gi), gl = __ldg(G.hh_gl + gi);
-                const double t_na = ld - w * (vk - __ldg(G.hh_ena + gi));
-                const double t_k = ld - w * (vk - __ldg(G.hh_ek + gi));
-                const double t_l = ld - w * (vk - __ldg(G.hh_el + gi));
-                const double m2h = m * m * h, n3 = nn * nn * nn;
-                GR.hh_gnabar[gi] += m2h * m * t_na;
-                GR.hh_gkbar[gi] += n3 * nn * t_k;
-                GR.hh_gl[gi] += t_l;
-                GR.hh_el[gi] += w * gl;
-                slm[i] += 3.0 * gnabar * m2h * t_na;
-                slh[i] += gnabar * m * m * m * t_na;
-                sln[i] += 4.0 * gkbar * n3 * t_k;
-                lvn -= w * (gnabar * m2h * m + gkbar * n3 * nn + gl);
+                slm[i] = lm;
+                slh[i] = lh;
+                sln[i] = ln;
             }
-            const int ic1 = __ldg(G.node_ic_off + gi + 1);
-            for (int k2 = __ldg(G.node_ic_off + gi); k2 < ic1; ++k2) {
-                const int j = __ldg(G.node_ic + k2);
-                const double del = __ldg(G.ic_del + j), dur = __ldg(G.ic_dur + j);
-                if (tm < del + dur && tm >= del) GR.ic_amp[j] += w * (1.e2 / __ldg(G.area + gi));
-            }
-            GR.cm[gi] += ld * G.cfac;
             const int par = M.par[i];
             if (par >= 0)
                 lvn += sb[i] * w - sa[i] * sw[par];

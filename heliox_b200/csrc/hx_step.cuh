@@ -295,45 +295,124 @@ __device__ __forceinline__ void assemble_net(const DevGroup& G, const DevNet& N,
     }
 }
 
+// Per-node mechanism parameters.  The loops over nodes load them for one node
+// with load_par at the top of an iteration, ahead of the arithmetic and of any
+// store, so that the global loads of an iteration are in flight together
+// rather than one round trip per mechanism.
+struct NodePar {
+    double pas_g, pas_e;
+    double gnabar, gkbar, gl, ena, ek, el;
+    double cm;
+    int ic0, ic1;  // the node's IClamp range in node_ic
+};
+
+__device__ __forceinline__ void load_par(const DevGroup& G, int gi, int fl, NodePar& q) {
+    q.pas_g = q.pas_e = 0.0;
+    q.gnabar = q.gkbar = q.gl = q.ena = q.ek = q.el = 0.0;
+    if (fl & kHasPas) {
+        q.pas_g = __ldg(G.pas_g + gi);
+        q.pas_e = __ldg(G.pas_e + gi);
+    }
+    if (fl & kHasHH) {
+        q.gnabar = __ldg(G.hh_gnabar + gi);
+        q.gkbar = __ldg(G.hh_gkbar + gi);
+        q.gl = __ldg(G.hh_gl + gi);
+        q.ena = __ldg(G.hh_ena + gi);
+        q.ek = __ldg(G.hh_ek + gi);
+        q.el = __ldg(G.hh_el + gi);
+    }
+    q.cm = __ldg(G.cm + gi);
+    q.ic0 = __ldg(G.node_ic_off + gi);
+    q.ic1 = __ldg(G.node_ic_off + gi + 1);
+}
+
+// Mechanism part of the VJP of step k at GPU node gi (pas, hh, IClamp,
+// capacitance): w = (M^-T mu)_i, ld = -w (v_{k+1} - v_k).  Accumulates the
+// parameter gradients, adds the gate adjoint increments to lm/lh/ln and
+// returns lvn minus the node's own conductance terms.  The gradient
+// accumulators and gates are loaded before the first store.
+__device__ __forceinline__ double vjp_mech(const DevGroup& G, const DevGrad& GR, const DevTape& T, size_t off, int i,
+                                           int gi, int fl, const NodePar& q, double w, double vk, double ld,
+                                           double tm, double lvn, double& lm, double& lh, double& ln) {
+    double m = 0.0, h = 0.0, nn = 0.0;
+    double a_pg = 0.0, a_pe = 0.0, a_na = 0.0, a_k = 0.0, a_l = 0.0, a_el = 0.0;
+    if (fl & kHasPas) {
+        a_pg = GR.pas_g[gi];
+        a_pe = GR.pas_e[gi];
+    }
+    if (fl & kHasHH) {
+        m = T.m[off + i];
+        h = T.h[off + i];
+        nn = T.n[off + i];
+        a_na = GR.hh_gnabar[gi];
+        a_k = GR.hh_gkbar[gi];
+        a_l = GR.hh_gl[gi];
+        a_el = GR.hh_el[gi];
+    }
+    const double a_cm = GR.cm[gi];
+    if (fl & kHasPas) {
+        GR.pas_g[gi] = a_pg + (ld - w * (vk - q.pas_e));
+        GR.pas_e[gi] = a_pe + w * q.pas_g;
+        lvn -= w * q.pas_g;
+    }
+    if (fl & kHasHH) {
+        const double t_na = ld - w * (vk - q.ena);
+        const double t_k = ld - w * (vk - q.ek);
+        const double t_l = ld - w * (vk - q.el);
+        const double m2h = m * m * h, n3 = nn * nn * nn;
+        GR.hh_gnabar[gi] = a_na + m2h * m * t_na;
+        GR.hh_gkbar[gi] = a_k + n3 * nn * t_k;
+        GR.hh_gl[gi] = a_l + t_l;
+        GR.hh_el[gi] = a_el + w * q.gl;
+        lm += 3.0 * q.gnabar * m2h * t_na;
+        lh += q.gnabar * m * m * m * t_na;
+        ln += 4.0 * q.gkbar * n3 * t_k;
+        lvn -= w * (q.gnabar * m2h * m + q.gkbar * n3 * nn + q.gl);
+    }
+    for (int k2 = q.ic0; k2 < q.ic1; ++k2) {
+        const int j = __ldg(G.node_ic + k2);
+        const double del = __ldg(G.ic_del + j), dur = __ldg(G.ic_dur + j);
+        if (tm < del + dur && tm >= del) GR.ic_amp[j] += w * (1.e2 / __ldg(G.area + gi));
+    }
+    GR.cm[gi] = a_cm + ld * G.cfac;
+    return lvn;
+}
+
 // rhs/d of pack-local node i in the reference's accumulation order:
 // pas, hh, IClamp (CoreNEURON type order), [network currents], capacitance
-// jacobian, axial terms.
+// jacobian, axial terms.  vi is the node's voltage; sv (neighbour voltages) is
+// read only when kRhs.
 template <bool kRhs, bool kNet = false, bool kSplitAxial = false>
-__device__ __forceinline__ void assemble(const DevGroup& G, const Meta& M, int pb, int i, int fl,
-                                         const double* __restrict__ sv, const double* __restrict__ sa,
+__device__ __forceinline__ void assemble(const DevGroup& G, const Meta& M, int pb, int i, int fl, const NodePar& q,
+                                         double vi, const double* __restrict__ sv, const double* __restrict__ sa,
                                          const double* __restrict__ sb, double m, double h, double n, double tmid,
                                          double& r_out, double& d_out, const DevNet& N = DevNet{},
                                          const double* synA = nullptr, const double* synB = nullptr, int syn0 = 0,
                                          const double* grs = nullptr, const double* vpeer = nullptr) {
     const int gi = pb + i;
-    const double vi = sv[i];
     double r = 0.0, dd = 0.0;
     if (fl & kHasPas) {  // pas_templated.cu:27-31 through MechTemp::current (FD conductance)
-        const double g = __ldg(G.pas_g + gi), e = __ldg(G.pas_e + gi);
-        double g1 = g * ((vi + kFdEps) - e);
-        const double i0 = g * (vi - e);
+        double g1 = q.pas_g * ((vi + kFdEps) - q.pas_e);
+        const double i0 = q.pas_g * (vi - q.pas_e);
         g1 = (g1 - i0) * kInvFdEps;
         r -= i0;
         dd += g1;
     }
     if (fl & kHasHH) {  // hh_templated.cu:137-149
-        const double gnabar = __ldg(G.hh_gnabar + gi), gkbar = __ldg(G.hh_gkbar + gi), gl = __ldg(G.hh_gl + gi);
-        const double ena = __ldg(G.hh_ena + gi), ek = __ldg(G.hh_ek + gi), el = __ldg(G.hh_el + gi);
-        double g1 = hh_current(vi + kFdEps, gnabar, gkbar, gl, m, h, n, ena, ek, el);
-        const double i0 = hh_current(vi, gnabar, gkbar, gl, m, h, n, ena, ek, el);
+        double g1 = hh_current(vi + kFdEps, q.gnabar, q.gkbar, q.gl, m, h, n, q.ena, q.ek, q.el);
+        const double i0 = hh_current(vi, q.gnabar, q.gkbar, q.gl, m, h, n, q.ena, q.ek, q.el);
         g1 = (g1 - i0) * kInvFdEps;
         r -= i0;
         dd += g1;
     }
-    const int ic1 = __ldg(G.node_ic_off + gi + 1);
-    for (int k = __ldg(G.node_ic_off + gi); k < ic1; ++k) {  // iclamp_templated.cu:35-45, electrode
+    for (int k = q.ic0; k < q.ic1; ++k) {  // iclamp_templated.cu:35-45, electrode
         const int j = __ldg(G.node_ic + k);
         const double del = __ldg(G.ic_del + j), dur = __ldg(G.ic_dur + j);
         const double cur = (tmid < del + dur && tmid >= del) ? __ldg(G.ic_amp + j) : 0.0;
         r += cur * (1.e2 / __ldg(G.area + gi));
     }
     if (kNet) assemble_net(G, N, gi, vi, synA, synB, syn0, grs, vpeer, r, dd);
-    dd += G.cfac * __ldg(G.cm + gi);
+    dd += G.cfac * q.cm;
     if (kSplitAxial) {  // parent / children may sit in other CTAs (a split cell)
         r_out = r;
         d_out = dd;
