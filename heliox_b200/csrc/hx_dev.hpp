@@ -43,9 +43,9 @@ struct DevTape {
 
 // Probe (recorded voltage) layout: per pack list of (pack-local node, column).
 struct DevProbe {
-    const int* pack_off;  // npack+1
-    const int* local;
-    const int* slot;
+    const int* slot_off;  // per cell slot (nslot+1): the slot's probes, sorted by (local node, probe index)
+    const int* local;     // pack-local node
+    const int* slot;      // output column
     int nprobe;
 };
 

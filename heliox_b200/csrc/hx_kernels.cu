@@ -67,10 +67,7 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_kernel(DevGroup G, DevState S
     double* sd = srhs + N_;
     double* sa = sd + N_;
     double* sb = sa + N_;
-    double* sgm = sb + N_;
-    double* sgh = sgm + N_;
-    double* sgn = sgh + N_;
-    double* ssA = sgn + N_;                       // kNet: synapse states of the pack
+    double* ssA = sb + N_;                        // kNet: synapse states of the pack
     double* ssB = ssA + (kNet ? N.smem_syn : 0);
     double* send = ssB + (kNet ? N.smem_syn : 0);
     Meta M;
@@ -82,9 +79,6 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_kernel(DevGroup G, DevState S
         sv[i] = S.v[pb + i];
         sa[i] = G.a[pb + i];
         sb[i] = G.b[pb + i];
-        sgm[i] = S.m[pb + i];
-        sgh[i] = S.h[pb + i];
-        sgn[i] = S.n[pb + i];
     }
     // kNet: the cell's synapses [c0, c1) (global ids), stored from ps0 in shared memory
     int c0 = 0, c1 = 0, ps0 = 0, psnode = -1, psflag = 0, gid = 0;
@@ -104,23 +98,14 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_kernel(DevGroup G, DevState S
             gid = N.cs_gid[g.slot];
         }
     }
-    const int q0 = P.pack_off[p], q1 = P.pack_off[p + 1];
+    const int q0 = P.slot_off[g.slot], q1 = P.slot_off[g.slot + 1];
     g.sync();
     if (k0 == 0 && trace)
-        for (int q = q0 + g.tl; q < q1; q += g.nt) {
-            const int l = P.local[q];
-            if (l >= i0 && l < i1) trace[P.slot[q]] = sv[l];
-        }
+        for (int q = q0 + g.tl; q < q1; q += g.nt) trace[P.slot[q]] = sv[P.local[q]];
     for (int k = k0; k < k1; ++k) {
-        if (write_tape) {
-            const size_t off = (size_t)(k - T.k_base) * (size_t)G.nnode + pb;
-            for (int i = i0 + g.tl; i < i1; i += g.nt) {
-                T.v[off + i] = sv[i];
-                T.m[off + i] = sgm[i];
-                T.h[off + i] = sgh[i];
-                T.n[off + i] = sgn[i];
-            }
-        }
+        const size_t toff = (size_t)(k - T.k_base) * (size_t)G.nnode + pb;
+        if (write_tape)
+            for (int i = i0 + g.tl; i < i1; i += g.nt) T.v[toff + i] = sv[i];
         if (kNet) {
             if (N.detect && g.tl == 0 && psnode >= 0) {
                 const double pv = sv[psnode];
@@ -152,11 +137,36 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_kernel(DevGroup G, DevState S
             }
         }
         const double tm = tmid[k];
-        // A: assembly
+        // A: gates of step k, tape row k, assembly.  The gates live in S.m/h/n;
+        // their cnexp update from v_k is applied here, one step late, so that
+        // they are read once per step together with the parameters (at the
+        // launch's first step S holds the current gates already).
         for (int i = i0 + g.tl; i < i1; i += g.nt) {
             const int fl = M.flag[i];
             NodePar q;
             load_par(G, pb + i, fl, q);
+            double gm = 0.0, gh = 0.0, gn = 0.0;
+            if (fl & kHasHH) {
+                gm = S.m[pb + i];
+                gh = S.h[pb + i];
+                gn = S.n[pb + i];
+            }
+            const double vi = sv[i];
+            if ((fl & kHasHH) && k > k0) {
+                HHRates rt;
+                hh_rates(vi, G.q10, rt);
+                gm = gate_step(gm, rt.inf[0], rt.k[0], G.dt);
+                gh = gate_step(gh, rt.inf[1], rt.k[1], G.dt);
+                gn = gate_step(gn, rt.inf[2], rt.k[2], G.dt);
+                S.m[pb + i] = gm;
+                S.h[pb + i] = gh;
+                S.n[pb + i] = gn;
+            }
+            if (write_tape && (fl & kHasHH)) {
+                T.m[toff + i] = gm;
+                T.h[toff + i] = gh;
+                T.n[toff + i] = gn;
+            }
             double r, dd;
             if (kNet) {
                 const int gi = pb + i;
@@ -175,10 +185,10 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_kernel(DevGroup G, DevState S
                         if (write_tape) N.tS[(size_t)(k - T.k_base + 1) * N.ngr + j] = sj;
                     }
                 }
-                assemble<true, true>(G, M, pb, i, fl, q, sv[i], sv, sa, sb, sgm[i], sgh[i], sgn[i], tm, r, dd, N,
-                                     ssA, ssB, ps0, N.gr_s, N.vpeer);
+                assemble<true, true>(G, M, pb, i, fl, q, vi, sv, sa, sb, gm, gh, gn, tm, r, dd, N, ssA, ssB, ps0,
+                                     N.gr_s, N.vpeer);
             } else {
-                assemble<true>(G, M, pb, i, fl, q, sv[i], sv, sa, sb, sgm[i], sgh[i], sgn[i], tm, r, dd);
+                assemble<true>(G, M, pb, i, fl, q, vi, sv, sa, sb, gm, gh, gn, tm, r, dd);
             }
             srhs[i] = r;
             sd[i] = dd;
@@ -186,17 +196,9 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_kernel(DevGroup G, DevState S
         g.sync();
         // B: Hines solve (rhs := dv)
         hines_cell<false>(M, g, sa, sb, sd, srhs);
-        // C: update + states
+        // C: v update (the gates follow in the next step's A, or below)
         for (int i = i0 + g.tl; i < i1; i += g.nt) {
-            const double vn = sv[i] + srhs[i];
-            sv[i] = vn;
-            if (M.flag[i] & kHasHH) {
-                HHRates r;
-                hh_rates(vn, G.q10, r);
-                sgm[i] = gate_step(sgm[i], r.inf[0], r.k[0], G.dt);
-                sgh[i] = gate_step(sgh[i], r.inf[1], r.k[1], G.dt);
-                sgn[i] = gate_step(sgn[i], r.inf[2], r.k[2], G.dt);
-            }
+            sv[i] = sv[i] + srhs[i];
             if (kNet) {  // synapse decay x + c (0 - x) (expsyn.cpp:125-134, exp2syn_temp.cuh:51-58)
                 const int s1 = __ldg(N.node_syn_off + pb + i + 1);
                 for (int j = __ldg(N.node_syn_off + pb + i); j < s1; ++j) {
@@ -208,10 +210,7 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_kernel(DevGroup G, DevState S
         }
         g.sync();
         if (trace)
-            for (int q = q0 + g.tl; q < q1; q += g.nt) {
-                const int l = P.local[q];
-                if (l >= i0 && l < i1) trace[(size_t)(k + 1) * P.nprobe + P.slot[q]] = sv[l];
-            }
+            for (int q = q0 + g.tl; q < q1; q += g.nt) trace[(size_t)(k + 1) * P.nprobe + P.slot[q]] = sv[P.local[q]];
     }
     if (write_tape) {
         const size_t off = (size_t)(k1 - T.k_base) * (size_t)G.nnode + pb;
@@ -220,9 +219,14 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_kernel(DevGroup G, DevState S
     double* vdst = (kNet && N.coupled) ? N.vout : S.v;
     for (int i = i0 + g.tl; i < i1; i += g.nt) {
         vdst[pb + i] = sv[i];
-        S.m[pb + i] = sgm[i];
-        S.h[pb + i] = sgh[i];
-        S.n[pb + i] = sgn[i];
+        if ((M.flag[i] & kHasHH) && k1 > k0) {  // gates of step k1 (the update the last step deferred)
+            const double gm = S.m[pb + i], gh = S.h[pb + i], gn = S.n[pb + i];
+            HHRates rt;
+            hh_rates(sv[i], G.q10, rt);
+            S.m[pb + i] = gate_step(gm, rt.inf[0], rt.k[0], G.dt);
+            S.h[pb + i] = gate_step(gh, rt.inf[1], rt.k[1], G.dt);
+            S.n[pb + i] = gate_step(gn, rt.inf[2], rt.k[2], G.dt);
+        }
     }
     if (kNet) {
         for (int j = c0 + g.tl; j < c1; j += g.nt) {
@@ -256,17 +260,14 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_kernel(DevGroup G, DevTape T,
     extern __shared__ double smem[];
     const int p = blockIdx.x;
     const int N_ = G.smem_n;
-    double* slv = smem;
-    double* sw = slv + N_;
+    // shared memory: the transposed system (w, d, a, b); the node adjoints
+    // lv, lm, lh, ln stay in Ad and v_k, v_{k+1} are read from the tape, each
+    // by the thread that owns the node
+    double* sw = smem;
     double* sd = sw + N_;
     double* sa = sd + N_;
     double* sb = sa + N_;
-    double* svk = sb + N_;
-    double* svk1 = svk + N_;
-    double* slm = svk1 + N_;
-    double* slh = slm + N_;
-    double* sln = slh + N_;
-    double* slA = sln + N_;  // kNet: synapse adjoints of the pack
+    double* slA = sb + N_;  // kNet: synapse adjoints of the pack
     double* slB = slA + (kNet ? N.smem_syn : 0);
     double* send = slB + (kNet ? N.smem_syn : 0);
     Meta M;
@@ -275,22 +276,22 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_kernel(DevGroup G, DevTape T,
     const int pb = G.pack_node_off[p];
     const int i0 = g.nb, i1 = g.nb + g.n;
     const double dt = G.dt, q10 = G.q10;
+    double* __restrict__ lv = Ad.lv + pb;
+    double* __restrict__ lmv = Ad.lm + pb;
+    double* __restrict__ lhv = Ad.lh + pb;
+    double* __restrict__ lnv = Ad.ln + pb;
     for (int i = i0 + g.tl; i < i1; i += g.nt) {
-        double l = Ad.lv[pb + i];
+        sa[i] = G.a[pb + i];
+        sb[i] = G.b[pb + i];
         if (kNet && N.coupled) {  // partner contributions to dL/dv_{k_hi} from the launch of step k_hi
+            double l = lv[i];
             const int e1 = __ldg(N.node_in_off + pb + i + 1);
             for (int e = __ldg(N.node_in_off + pb + i); e < e1; ++e) {
                 const int code = __ldg(N.node_in + e), kind = code >> 28, inst = code & 0x0FFFFFFF;
                 l += (kind == 0 ? N.x_hg_in : kind == 1 ? N.x_gj_in : N.x_gr_in)[inst];
             }
+            lv[i] = l;
         }
-        slv[i] = l;
-        sa[i] = G.a[pb + i];
-        sb[i] = G.b[pb + i];
-        slm[i] = Ad.lm[pb + i];
-        slh[i] = Ad.lh[pb + i];
-        sln[i] = Ad.ln[pb + i];
-        svk1[i] = T.v[(size_t)(k_hi - T.k_base) * (size_t)G.nnode + pb + i];
     }
     int c0 = 0, c1 = 0, ps0 = 0;
     if (kNet) {
@@ -302,16 +303,15 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_kernel(DevGroup G, DevTape T,
             slB[j - ps0] = Ad.lB[j];
         }
     }
-    const int q0 = P.pack_off[p], q1 = P.pack_off[p + 1];
+    const int q0 = P.slot_off[g.slot], q1 = P.slot_off[g.slot + 1];
     g.sync();
     for (int k = k_hi - 1; k >= k_lo; --k) {
         const size_t off = (size_t)(k - T.k_base) * (size_t)G.nnode + pb;
-        for (int i = i0 + g.tl; i < i1; i += g.nt) svk[i] = T.v[off + i];
-        if (g.tl == 0)
-            for (int q = q0; q < q1; ++q) {
-                const int l = P.local[q];
-                if (l >= i0 && l < i1) slv[l] += dLdv[(size_t)(k + 1) * P.nprobe + P.slot[q]];
-            }
+        if (k > k_lo && g.tl < 4) {  // the next step's tape rows of the cell, into L2
+            const double* row = (g.tl == 0 ? T.v : g.tl == 1 ? T.m : g.tl == 2 ? T.h : T.n) + off - G.nnode + i0;
+            prefetch_l2(row, sizeof(double) * (size_t)(i1 - i0));
+        }
+        probe_inject(P, q0, q1, dLdv + (size_t)(k + 1) * P.nprobe, lv, g);
         g.sync();
         const double tm = tmid[k];
         const double* tA = kNet ? N.tA + (size_t)(k - T.k_base) * (size_t)N.nsyn : nullptr;
@@ -320,17 +320,19 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_kernel(DevGroup G, DevTape T,
         const double* vpeer = T.v + (size_t)(k - T.k_base) * (size_t)G.nnode;
         // S + A
         for (int i = i0 + g.tl; i < i1; i += g.nt) {
-            double mu = slv[i];
             const int fl = M.flag[i];
+            double mu = lv[i];
+            const double vk = T.v[off + i];
             double gm = 0.0, gh = 0.0, gn = 0.0;
             if (fl & kHasHH) {
+                const double v1 = T.v[off + G.nnode + i];
                 gm = T.m[off + i];
                 gh = T.h[off + i];
                 gn = T.n[off + i];
+                double lam[3] = {lmv[i], lhv[i], lnv[i]};
                 HHRatesD R;
-                hh_rates_d(svk1[i], q10, R);
+                hh_rates_d(v1, q10, R);
                 const double x[3] = {gm, gh, gn};
-                double lam[3] = {slm[i], slh[i], sln[i]};
 #pragma unroll
                 for (int q = 0; q < 3; ++q) {
                     const double E = exp(-dt * R.k[q]);
@@ -338,9 +340,9 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_kernel(DevGroup G, DevTape T,
                     mu += lam[q] * dnew;
                     lam[q] *= E;
                 }
-                slm[i] = lam[0];
-                slh[i] = lam[1];
-                sln[i] = lam[2];
+                lmv[i] = lam[0];
+                lhv[i] = lam[1];
+                lnv[i] = lam[2];
             }
             // (parameters loaded after the rate chain: held across it they spill)
             NodePar q;
@@ -352,14 +354,14 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_kernel(DevGroup G, DevTape T,
                     slA[j - ps0] *= 1.0 - __ldg(N.syn_cA + j);
                     slB[j - ps0] *= 1.0 - __ldg(N.syn_cB + j);
                 }
-                assemble<false, true>(G, M, pb, i, fl, q, svk[i], svk, sa, sb, gm, gh, gn, tm, r, dd, N, tA, tB, 0,
+                assemble<false, true>(G, M, pb, i, fl, q, vk, nullptr, sa, sb, gm, gh, gn, tm, r, dd, N, tA, tB, 0,
                                       grs, vpeer);
             } else {
-                assemble<false>(G, M, pb, i, fl, q, svk[i], svk, sa, sb, gm, gh, gn, tm, r, dd);
+                assemble<false>(G, M, pb, i, fl, q, vk, nullptr, sa, sb, gm, gh, gn, tm, r, dd);
             }
             sd[i] = dd;
             sw[i] = mu;
-            slv[i] = mu;
+            lv[i] = mu;
         }
         g.sync();
         // B: w = M^{-T} mu
@@ -371,15 +373,20 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_kernel(DevGroup G, DevTape T,
             NodePar q;
             load_par(G, gi, fl, q);
             const double w = sw[i];
-            const double vk = svk[i];
-            const double ld = -w * (svk1[i] - vk);
-            const double lvn0 = slv[i];
-            double lm = slm[i], lh = slh[i], ln = sln[i];
+            const double vk = T.v[off + i];
+            const double ld = -w * (T.v[off + G.nnode + i] - vk);
+            const double lvn0 = lv[i];
+            double lm = 0.0, lh = 0.0, ln = 0.0;
+            if (fl & kHasHH) {
+                lm = lmv[i];
+                lh = lhv[i];
+                ln = lnv[i];
+            }
             double lvn = vjp_mech(G, GR, T, off, i, gi, fl, q, w, vk, ld, tm, lvn0, lm, lh, ln);
             if (fl & kHasHH) {
-                slm[i] = lm;
-                slh[i] = lh;
-                sln[i] = ln;
+                lmv[i] = lm;
+                lhv[i] = lh;
+                lnv[i] = ln;
             }
             if (kNet) {
                 const double sarea = 1.e2 / __ldg(G.area + gi);
@@ -445,7 +452,7 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_kernel(DevGroup G, DevTape T,
                 const int c = M.ch[k2];
                 lvn += sa[c] * w - sb[c] * sw[c];
             }
-            slv[i] = lvn;
+            lv[i] = lvn;
         }
         if (kNet) {  // event weight gradients: dL/dw += fA lA' + fB lB' per delivery at step k
             g.sync();
@@ -457,16 +464,7 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_kernel(DevGroup G, DevTape T,
                     atomicAdd(GR.syn_w + j, __ldg(N.syn_fA + j) * slA[j - ps0] + __ldg(N.syn_fB + j) * slB[j - ps0]);
             }
         }
-        double* tmp = svk1;
-        svk1 = svk;
-        svk = tmp;
         g.sync();
-    }
-    for (int i = i0 + g.tl; i < i1; i += g.nt) {
-        Ad.lv[pb + i] = slv[i];
-        Ad.lm[pb + i] = slm[i];
-        Ad.lh[pb + i] = slh[i];
-        Ad.ln[pb + i] = sln[i];
     }
     if (kNet)
         for (int j = c0 + g.tl; j < c1; j += g.nt) {
@@ -602,15 +600,15 @@ cudaError_t launch_f32_to_f64(const float* a, double* b, int n, cudaStream_t st)
 }
 
 // ------------------------------------------------------------------ launchers
-static size_t meta_bytes(const DevGroup& G) {
-    return sizeof(int) * (3 * (size_t)G.smem_n + 1 + G.smem_nch + 4 * (size_t)G.smem_br + 1 + G.smem_bch + G.smem_lvl);
-}
 size_t fwd_smem_bytes(const DevGroup& G, int smem_syn) {
-    return sizeof(double) * (8 * (size_t)G.smem_n + 2 * (size_t)smem_syn) + meta_bytes(G);
+    return sizeof(double) * (5 * (size_t)G.smem_n + 2 * (size_t)smem_syn) + meta_bytes(G);
 }
 size_t bwd_smem_bytes(const DevGroup& G, int smem_syn) {
-    return sizeof(double) * (10 * (size_t)G.smem_n + 2 * (size_t)smem_syn) + meta_bytes(G);
+    return sizeof(double) * (4 * (size_t)G.smem_n + 2 * (size_t)smem_syn) + meta_bytes(G);
 }
+// split-cell kernels (hx_split.cu) keep the gates / node adjoints in shared memory
+size_t split_fwd_smem_bytes(const DevGroup& G) { return sizeof(double) * 8 * (size_t)G.smem_n + meta_bytes(G); }
+size_t split_bwd_smem_bytes(const DevGroup& G) { return sizeof(double) * 10 * (size_t)G.smem_n + meta_bytes(G); }
 
 cudaError_t configure_kernels(size_t smem_fwd, size_t smem_bwd, size_t smem_fwd_net, size_t smem_bwd_net) {
     cudaError_t e = cudaFuncSetAttribute(fwd_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_fwd);

@@ -9,6 +9,8 @@ namespace hx {
 
 size_t fwd_smem_bytes(const DevGroup& G, int smem_syn = 0);
 size_t bwd_smem_bytes(const DevGroup& G, int smem_syn = 0);
+size_t split_fwd_smem_bytes(const DevGroup& G);
+size_t split_bwd_smem_bytes(const DevGroup& G);
 cudaError_t configure_kernels(size_t smem_fwd, size_t smem_bwd, size_t smem_fwd_net, size_t smem_bwd_net);
 cudaError_t launch_init(const DevGroup& G, const DevState& S, double v_init, cudaStream_t st);
 // N == nullptr: the plain kernels; otherwise the network instantiation

@@ -6,6 +6,7 @@
 #include <cstdint>
 #include <numeric>
 #include <queue>
+#include <set>
 #include <sstream>
 #include <unordered_map>
 
@@ -145,7 +146,7 @@ std::string split_cell(const std::vector<Branch>& Bin, const std::vector<int>& p
 
 }  // namespace
 
-std::string build_plan(const hx_group_desc& g, int nodes_per_warp, int max_pack_nodes, Plan& P) {
+std::string build_plan(const hx_group_desc& g, int nodes_per_warp, int max_pack_nodes, Plan& P, int nsm) {
     std::string err = validate(g);
     if (!err.empty()) return err;
     P = Plan();
@@ -233,14 +234,20 @@ std::string build_plan(const hx_group_desc& g, int nodes_per_warp, int max_pack_
     }
     const int nunit = (int)ubr.size();
 
-    // first-fit-decreasing packing of whole cells into CTAs by node count (the
-    // shared-memory capacity; at most kWarpsPerCta cells), then the CTA's warps
-    // are shared among its cells in proportion to their nodes (at least one
-    // each, largest remainders first), so every thread of a CTA carries about
-    // the same number of nodes.
+    // Whole cells are packed into CTAs (at most kWarpsPerCta cells and the
+    // shared-memory capacity in nodes each); the CTA's warps are then shared
+    // among its cells in proportion to their nodes (at least one each, largest
+    // remainders first), so every thread of a CTA carries about the same
+    // number of nodes.
+    //   nsm > 0 (and no explicit nodes_per_warp): one CTA per SM, as few waves
+    //     as the capacity allows -- cells are dealt largest first to the least
+    //     loaded of nsm * waves CTAs (LPT), so the CTAs of a wave finish together;
+    //   otherwise: first-fit decreasing into CTAs of nodes_per_warp * warps
+    //     (default 144 nodes per warp) nodes.
+    const bool balanced = nodes_per_warp <= 0 && nsm > 0 && max_pack_nodes > 0;
     const int npw = nodes_per_warp > 0 ? nodes_per_warp : 144;
     const int maxcell = *std::max_element(usize.begin(), usize.end());
-    int cap = npw * kWarpsPerCta;
+    int cap = balanced ? max_pack_nodes : npw * kWarpsPerCta;
     if (max_pack_nodes > 0) {
         if (maxcell > max_pack_nodes)
             return "a cell of " + std::to_string(maxcell) + " nodes exceeds the per-CTA capacity of " +
@@ -259,20 +266,68 @@ std::string build_plan(const hx_group_desc& g, int nodes_per_warp, int max_pack_
         bins.push_back({top_unit});
         bin_n.push_back(usize[top_unit]);
     }
-    for (int c : order) {
-        int b = -1;
-        for (int k = top_unit >= 0 ? 1 : 0; k < (int)bins.size(); k++)
-            if ((int)bins[k].size() < kWarpsPerCta && bin_n[k] + usize[c] <= cap) {
-                b = k;
-                break;
-            }
-        if (b < 0) {
+    const int b0 = (int)bins.size();
+    if (balanced && !order.empty()) {
+        long long total = 0;
+        for (int c : order) total += usize[c];
+        const int avail = std::max(1, nsm - b0);
+        // waves: enough CTA capacity with a few percent left for fragmentation
+        const long long per_wave = (long long)avail * (long long)(cap * 0.96);
+        int waves = (int)std::max<long long>(1, (total + per_wave - 1) / std::max<long long>(per_wave, 1));
+        long long K = (long long)avail * waves;
+        K = std::max<long long>(K, ((long long)order.size() + kWarpsPerCta - 1) / kWarpsPerCta);
+        K = std::min<long long>(K, (long long)order.size());
+        std::set<std::pair<long long, int>> load;  // (nodes, bin)
+        for (long long k = 0; k < K; k++) {
             bins.push_back({});
             bin_n.push_back(0);
-            b = (int)bins.size() - 1;
+            load.insert({0, (int)(b0 + k)});
         }
-        bins[b].push_back(c);
-        bin_n[b] += usize[c];
+        for (int c : order) {
+            int b = -1;
+            for (auto it = load.begin(); it != load.end(); ++it) {
+                const int k = it->second;
+                if ((int)bins[k].size() < kWarpsPerCta && bin_n[k] + usize[c] <= cap) {
+                    b = k;
+                    load.erase(it);
+                    break;
+                }
+            }
+            if (b < 0) {
+                bins.push_back({});
+                bin_n.push_back(0);
+                b = (int)bins.size() - 1;
+            }
+            bins[b].push_back(c);
+            bin_n[b] += usize[c];
+            if ((int)bins[b].size() < kWarpsPerCta) load.insert({bin_n[b], b});
+        }
+        // drop bins left empty (fewer units than CTAs)
+        std::vector<std::vector<int>> kept;
+        std::vector<int> kept_n;
+        for (size_t k = 0; k < bins.size(); k++)
+            if (!bins[k].empty()) {
+                kept.push_back(std::move(bins[k]));
+                kept_n.push_back(bin_n[k]);
+            }
+        bins.swap(kept);
+        bin_n.swap(kept_n);
+    } else {
+        for (int c : order) {
+            int b = -1;
+            for (int k = b0; k < (int)bins.size(); k++)
+                if ((int)bins[k].size() < kWarpsPerCta && bin_n[k] + usize[c] <= cap) {
+                    b = k;
+                    break;
+                }
+            if (b < 0) {
+                bins.push_back({});
+                bin_n.push_back(0);
+                b = (int)bins.size() - 1;
+            }
+            bins[b].push_back(c);
+            bin_n[b] += usize[c];
+        }
     }
     for (size_t b = 0; b < bins.size(); b++) {
         const int nb = (int)bins[b].size();

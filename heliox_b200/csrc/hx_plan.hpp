@@ -71,8 +71,10 @@ struct Plan {
 
 // Validates the group and builds the plan.  nodes_per_warp: target cell nodes
 // per warp (0 = default); max_pack_nodes: node capacity of one CTA (shared
-// memory), 0 = unlimited.  Returns "" on success, else a reason.
-std::string build_plan(const hx_group_desc& g, int nodes_per_warp, int max_pack_nodes, Plan& out);
+// memory), 0 = unlimited; nsm: SMs of the device (0 = unknown).  With nsm and
+// a capacity but no explicit nodes_per_warp the CTAs are balanced over whole
+// waves of nsm CTAs.  Returns "" on success, else a reason.
+std::string build_plan(const hx_group_desc& g, int nodes_per_warp, int max_pack_nodes, Plan& out, int nsm = 0);
 
 // CPU emulation of the kernels' planned Hines solve on GPU-ordered arrays
 // (a, b, d, rhs are GPU-ordered and pack-contiguous).  transposed swaps a/b.

@@ -252,18 +252,28 @@ int hx_load_group(hx_ctx* ctx, const hx_group_desc* desc) {
     ctx->captured = false;
     ctx->probe_key.clear();
     ctx->tmid_steps = -1;
-    // per-CTA node capacity from the opt-in shared memory (backward kernel: 10
-    // doubles per node plus the topology tables, about 16 bytes per node)
-    int optin = 0;
+    // per-CTA node capacity from the opt-in shared memory: the forward kernel
+    // keeps 5 doubles per node (the backward 4) plus about 10 bytes of
+    // topology tables; network groups add 2 doubles per synapse of the pack,
+    // budgeted at 1.5x the group's mean synapse density.  A single cell larger
+    // than that is split across CTAs, whose kernels keep 10 doubles per node.
+    // The plan is checked against the exact table sizes and rebuilt with a
+    // smaller capacity while it does not fit.
+    int optin = 0, nsm = 0;
     HXC(cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, ctx->device));
-    // (network groups: plus 2 doubles per synapse in the pack, budgeted at 1.5x
-    // the group's mean synapse density; a pack that still overflows shrinks the cap)
+    HXC(cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, ctx->device));
     const double syn_per_node =
         desc->nnode > 0 ? (double)(std::max(desc->nexpsyn, 0) + std::max(desc->nexp2syn, 0)) / desc->nnode : 0.0;
-    int cap_nodes = (int)((optin - 4096) / (10 * sizeof(double) + 20 + 1.5 * 16 * syn_per_node));
-    std::string e = hx::build_plan(*desc, ctx->pack_target, cap_nodes, ctx->P);
+    int cap_nodes = (int)((optin - 4096) / (5 * sizeof(double) + 10 + 1.5 * 16 * syn_per_node));
+    bool split_kernels = false;
+    if (desc->ncell == 1 && desc->nnode > cap_nodes) {
+        split_kernels = true;
+        cap_nodes = (int)((optin - 4096) / (10 * sizeof(double) + 10));
+    }
+    cap_nodes = std::min(cap_nodes, 32767);  // 16-bit node tables
+    std::string e = hx::build_plan(*desc, ctx->pack_target, cap_nodes, ctx->P, nsm);
     if (!e.empty()) return fail(ctx, "invalid group: " + e);
-    for (int shrink = 0; shrink < 6 && desc->nnode > 0; shrink++) {
+    for (int shrink = 0; shrink < 8 && desc->nnode > 0; shrink++) {
         // largest synapse count of any pack under this plan
         const hx::Plan& Pc = ctx->P;
         std::vector<int> nsyn_node(Pc.nnode, 0);
@@ -275,10 +285,17 @@ int hx_load_group(hx_ctx* ctx, const hx_group_desc* desc) {
             for (int gi = Pc.pack_node_off[p]; gi < Pc.pack_node_off[p + 1]; gi++) s += nsyn_node[gi];
             worst = std::max(worst, s);
         }
-        const size_t need = (size_t)Pc.max_pack_nodes * (10 * sizeof(double) + 20) + 16 * (size_t)worst + 4096;
+        hx::DevGroup Gt{};
+        Gt.smem_n = std::max(Pc.max_pack_nodes, 1);
+        Gt.smem_br = Pc.max_pack_branches;
+        Gt.smem_bch = Pc.max_pack_bch;
+        Gt.smem_nch = Pc.max_pack_nch;
+        Gt.smem_lvl = hx::kWarpsPerCta * (Pc.max_levels + 1);
+        const size_t need = split_kernels ? std::max(hx::split_fwd_smem_bytes(Gt), hx::split_bwd_smem_bytes(Gt))
+                                          : std::max(hx::fwd_smem_bytes(Gt, worst), hx::bwd_smem_bytes(Gt, worst));
         if (need <= (size_t)optin) break;
-        cap_nodes = (int)(cap_nodes * 0.9);
-        e = hx::build_plan(*desc, ctx->pack_target, cap_nodes, ctx->P);
+        cap_nodes = (int)(cap_nodes * 0.92);
+        e = hx::build_plan(*desc, ctx->pack_target, cap_nodes, ctx->P, nsm);
         if (!e.empty()) return fail(ctx, "invalid group: " + e);
     }
     const hx::Plan& P = ctx->P;
@@ -428,22 +445,23 @@ int hx_load_group(hx_ctx* ctx, const hx_group_desc* desc) {
     G.dt = desc->dt;
     G.cfac = 0.001 * (1.0 / desc->dt);                  // capac.cpp:56,70 with cj = 1/dt
     G.q10 = std::pow(3.0, (desc->celsius - 6.3) / 10);  // hh_templated.cu:90
-    size_t sf = hx::fwd_smem_bytes(G), sb = hx::bwd_smem_bytes(G);
+    ctx->split = P.nsub > 0;
+    size_t sf = ctx->split ? hx::split_fwd_smem_bytes(G) : hx::fwd_smem_bytes(G);
+    size_t sb = ctx->split ? hx::split_bwd_smem_bytes(G) : hx::bwd_smem_bytes(G);
     size_t sfn = hx::fwd_smem_bytes(G, ctx->N.smem_syn), sbn = hx::bwd_smem_bytes(G, ctx->N.smem_syn);
     int maxsmem = 0;
     HXC(cudaDeviceGetAttribute(&maxsmem, cudaDevAttrMaxSharedMemoryPerBlockOptin, ctx->device));
-    const size_t need = ctx->net ? sbn : sb;
-    if (need > (size_t)maxsmem || sf > (size_t)maxsmem)
+    const size_t need = std::max(ctx->net ? std::max(sfn, sbn) : sb, sf);
+    if (need > (size_t)maxsmem)
         return fail(ctx, "cell pack needs " + std::to_string(need) + " B shared memory (> " + std::to_string(maxsmem) +
                              "); lower the pack target or split the cell");
-    HXC(hx::configure_kernels(sf, sb, std::min(sfn, (size_t)maxsmem), std::min(sbn, (size_t)maxsmem)));
-    ctx->split = P.nsub > 0;
+    HXC(hx::configure_kernels(std::min(hx::fwd_smem_bytes(G), (size_t)maxsmem),
+                              std::min(hx::bwd_smem_bytes(G), (size_t)maxsmem), std::min(sfn, (size_t)maxsmem),
+                              std::min(sbn, (size_t)maxsmem)));
     if (ctx->split) {
         if (ctx->net) return fail(ctx, "a cell split across CTAs cannot carry network parts");
         HXC(hx::configure_split(sf, sb));
-        int per_sm = 0, nsm = 0;
-        HXC(cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, ctx->device));
-        int per_sm_b = 0;
+        int per_sm = 0, per_sm_b = 0;
         HXC(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, hx::split_fwd_kernel_ptr(), hx::kThreads, sf));
         HXC(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm_b, hx::split_bwd_kernel_ptr(), hx::kThreads, sb));
         if ((long long)std::min(per_sm, per_sm_b) * nsm < P.npack)
@@ -526,21 +544,32 @@ int hx_setup_probes(hx_ctx* ctx, int nprobe, const int* probe_nodes) {
     const hx::Plan& P = ctx->P;
     std::vector<int> key(probe_nodes, probe_nodes + nprobe);
     if (key == ctx->probe_key && ctx->pr_off.p) return 0;
-    std::vector<std::vector<std::pair<int, int>>> per(P.npack);
+    // cell slot of every GPU node
+    const int nslot = (int)P.cs_node0.size();
+    std::vector<int> node_slot(P.nnode, -1);
+    for (int p = 0; p < P.npack; p++)
+        for (int s = P.pack_slot_off[p]; s < P.pack_slot_off[p + 1]; s++)
+            for (int l = P.cs_node0[s]; l < P.cs_node0[s] + P.cs_nnode[s]; l++) node_slot[P.pack_node_off[p] + l] = s;
+    // per slot, sorted by (pack-local node, probe index): a node's probes form
+    // one run, summed in probe order by one thread in the backward
+    std::vector<std::vector<std::pair<int, int>>> per(nslot);
     for (int q = 0; q < nprobe; q++) {
         int r = probe_nodes[q];
         if (r < 0 || r >= P.nnode) return fail(ctx, "probe node out of range");
         int gi = P.ref2gpu[r];
         int pk = (int)(std::upper_bound(P.pack_node_off.begin(), P.pack_node_off.end(), gi) - P.pack_node_off.begin()) - 1;
-        per[pk].push_back({gi - P.pack_node_off[pk], q});
+        if (node_slot[gi] < 0) return fail(ctx, "probe node outside every cell slot");
+        per[node_slot[gi]].push_back({gi - P.pack_node_off[pk], q});
     }
-    std::vector<int> off(P.npack + 1, 0), loc, slot;
-    for (int p = 0; p < P.npack; p++) {
-        for (auto& pr : per[p]) {
+    std::vector<int> off(nslot + 1, 0), loc, slot;
+    for (int s = 0; s < nslot; s++) {
+        std::stable_sort(per[s].begin(), per[s].end(),
+                         [](const std::pair<int, int>& x, const std::pair<int, int>& y) { return x.first < y.first; });
+        for (auto& pr : per[s]) {
             loc.push_back(pr.first);
             slot.push_back(pr.second);
         }
-        off[p + 1] = (int)loc.size();
+        off[s + 1] = (int)loc.size();
     }
     if (loc.empty()) {
         loc.push_back(0);
@@ -556,7 +585,7 @@ int hx_setup_probes(hx_ctx* ctx, int nprobe, const int* probe_nodes) {
 
 hx::DevProbe hx_probe_view(hx_ctx* c) {
     hx::DevProbe p;
-    p.pack_off = c->pr_off.p;
+    p.slot_off = c->pr_off.p;
     p.local = c->pr_local.p;
     p.slot = c->pr_slot.p;
     p.nprobe = c->nprobe;

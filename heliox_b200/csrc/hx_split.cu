@@ -205,13 +205,10 @@ __global__ void __launch_bounds__(kThreads, 1) split_fwd_kernel(DevGroup G, DevS
         }
         g.sync();
     }
-    const int q0 = P.pack_off[p], q1 = P.pack_off[p + 1];
+    const int q0 = active ? P.slot_off[g.slot] : 0, q1 = active ? P.slot_off[g.slot + 1] : 0;
     auto trace_row = [&](int row) {
         if (!trace) return;
-        for (int q = q0 + g.tl; q < q1; q += g.nt) {
-            const int l = P.local[q];
-            if (l >= i0 && l < i1) trace[(size_t)row * P.nprobe + P.slot[q]] = sv[l];
-        }
+        for (int q = q0 + g.tl; q < q1; q += g.nt) trace[(size_t)row * P.nprobe + P.slot[q]] = sv[P.local[q]];
     };
     auto tape_row = [&](int k) {
         if (!write_tape) return;
@@ -352,16 +349,12 @@ __global__ void __launch_bounds__(kThreads, 1) split_bwd_kernel(DevGroup G, DevT
         }
         g.sync();
     }
-    const int q0 = P.pack_off[p], q1 = P.pack_off[p + 1];
+    const int q0 = active ? P.slot_off[g.slot] : 0, q1 = active ? P.slot_off[g.slot + 1] : 0;
     // lv += dL/dv_{k+1} at the probes, tape v_k into svk, S+A phase, transposed elimination
     auto stage1 = [&](int k) {
         const size_t off = (size_t)(k - T.k_base) * (size_t)G.nnode + pb;
-        for (int i = i0 + g.tl; i < i1; i += g.nt) svk[i] = T.v[off + i];
-        if (g.tl == 0)
-            for (int q = q0; q < q1; ++q) {
-                const int l = P.local[q];
-                if (l >= i0 && l < i1) slv[l] += dLdv[(size_t)(k + 1) * P.nprobe + P.slot[q]];
-            }
+        copy_in(svk, T.v + off, i0, i1, g);
+        probe_inject(P, q0, q1, dLdv + (size_t)(k + 1) * P.nprobe, slv, g);
         g.sync();
         const double tm = tmid[k];
         for (int i = i0 + g.tl; i < i1; i += g.nt) {
@@ -500,7 +493,7 @@ cudaError_t launch_split_fwd(const DevGroup& G, const DevState& S, const DevTape
     DevSplit x = X;
     void* args[] = {&g, &s, &t, &write_tape, &pr, &trace, &tmid, &k0, &k1, &x};
     return cudaLaunchCooperativeKernel((const void*)split_fwd_kernel, dim3(G.npack), dim3(kThreads), args,
-                                       fwd_smem_bytes(G, 0), st);
+                                       split_fwd_smem_bytes(G), st);
 }
 
 cudaError_t launch_split_bwd(const DevGroup& G, const DevTape& T, const DevAdj& A, const DevGrad& GR, const DevProbe& P,
@@ -514,7 +507,7 @@ cudaError_t launch_split_bwd(const DevGroup& G, const DevTape& T, const DevAdj& 
     DevSplit x = X;
     void* args[] = {&g, &t, &a, &gr, &pr, &dLdv, &tmid, &k_hi, &k_lo, &x};
     return cudaLaunchCooperativeKernel((const void*)split_bwd_kernel, dim3(G.npack), dim3(kThreads), args,
-                                       bwd_smem_bytes(G, 0), st);
+                                       split_bwd_smem_bytes(G), st);
 }
 
 }  // namespace hx

@@ -106,12 +106,14 @@ __device__ __forceinline__ void back_block(const double* __restrict__ d, double*
 }
 
 // ------------------------------------------------------------------ cell groups
-// Shared-memory copies of the pack's topology and schedule (int tables).
+// Shared-memory copies of the pack's topology and schedule.  Node tables are
+// 16-bit (pack-local ids and offsets; a pack holds at most 32767 nodes) and the
+// node flags 8-bit; the branch tables are ints.
 struct Meta {
-    int* par;   // node parent (pack-local), -1 for roots
-    int* flag;  // NodeFlag bits
-    int* cho;   // node child offsets into ch (size n+1)
-    int* ch;    // node children (pack-local), ascending reference index
+    short* par;           // node parent (pack-local), -1 for roots, -(2 + subtree) across CTAs
+    unsigned char* flag;  // NodeFlag bits
+    short* cho;           // node child offsets into ch (size n+1)
+    short* ch;            // node children (pack-local), ascending reference index
     int* bh;    // branch head / end / head's parent (pack-local nodes)
     int* be;
     int* bp;
@@ -135,24 +137,28 @@ struct Grp {
     }
 };
 
-__device__ __forceinline__ size_t meta_ints(const DevGroup& G) {
-    return 3 * (size_t)G.smem_n + 1 + G.smem_nch + 4 * (size_t)G.smem_br + 1 + G.smem_bch + G.smem_lvl;
+// Bytes of the Meta tables in shared memory (a multiple of 16).
+__host__ __device__ inline size_t meta_bytes(const DevGroup& G) {
+    const size_t ints = 4 * (size_t)G.smem_br + 1 + G.smem_bch + G.smem_lvl;
+    const size_t shorts = 2 * (size_t)G.smem_n + 1 + G.smem_nch;
+    const size_t b = 4 * ints + 2 * shorts + (size_t)G.smem_n;
+    return (b + 15) & ~(size_t)15;
 }
 
 // Loads the pack's tables into shared memory (whole CTA), then returns the
 // calling thread's cell group; false for warps the pack leaves idle.
 __device__ __forceinline__ bool setup_pack(const DevGroup& G, int p, int* ibase, Meta& M, Grp& g) {
     const int tid = threadIdx.x, nt = blockDim.x;
-    M.par = ibase;
-    M.flag = M.par + G.smem_n;
-    M.cho = M.flag + G.smem_n;
-    M.ch = M.cho + G.smem_n + 1;
-    M.bh = M.ch + G.smem_nch;
+    M.bh = ibase;
     M.be = M.bh + G.smem_br;
     M.bp = M.be + G.smem_br;
     M.bco = M.bp + G.smem_br;
     M.bc = M.bco + G.smem_br + 1;
     M.lvl = M.bc + G.smem_bch;
+    M.par = reinterpret_cast<short*>(M.lvl + G.smem_lvl);
+    M.cho = M.par + G.smem_n;
+    M.ch = M.cho + G.smem_n + 1;
+    M.flag = reinterpret_cast<unsigned char*>(M.ch + G.smem_nch);
     const int pb = G.pack_node_off[p], pn = G.pack_node_off[p + 1] - pb;
     const int nch0 = G.pack_nch_off[p], nch = G.pack_nch_off[p + 1] - nch0;
     const int br0 = G.pack_br_off[p], nbr = G.pack_br_off[p + 1] - br0;
@@ -160,12 +166,12 @@ __device__ __forceinline__ bool setup_pack(const DevGroup& G, int p, int* ibase,
     const int s0 = G.pack_slot_off[p], s1 = G.pack_slot_off[p + 1];
     const int l0 = G.cs_lvl_off[s0], l1 = G.cs_lvl_off[s1 - 1] + G.cs_nlev[s1 - 1] + 1;
     for (int i = tid; i < pn; i += nt) {
-        M.par[i] = G.node_parent[pb + i];
-        M.flag[i] = G.node_flags[pb + i];
-        M.cho[i] = G.node_child_off[pb + i] - nch0;
+        M.par[i] = (short)G.node_parent[pb + i];
+        M.flag[i] = (unsigned char)G.node_flags[pb + i];
+        M.cho[i] = (short)(G.node_child_off[pb + i] - nch0);
     }
-    if (tid == 0) M.cho[pn] = nch;
-    for (int k = tid; k < nch; k += nt) M.ch[k] = G.node_child[nch0 + k];
+    if (tid == 0) M.cho[pn] = (short)nch;
+    for (int k = tid; k < nch; k += nt) M.ch[k] = (short)G.node_child[nch0 + k];
     for (int k = tid; k < nbr; k += nt) {
         M.bh[k] = G.br_head[br0 + k];
         M.be[k] = G.br_end[br0 + k];
@@ -244,6 +250,49 @@ __device__ __forceinline__ void hines_cell(const Meta& M, const Grp& g, const do
         }
         g.sync();
     }
+}
+
+// ------------------------------------------------------------------ per-step I/O
+// dst[i] = src[i] for the group's nodes i = i0 + tl + j*nt, four loads in flight
+// per thread before the stores.
+__device__ __forceinline__ void copy_in(double* __restrict__ dst, const double* __restrict__ src, int i0, int i1,
+                                        const Grp& g) {
+    for (int i = i0 + g.tl; i < i1; i += 4 * g.nt) {
+        double x[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            const int j = i + u * g.nt;
+            x[u] = j < i1 ? src[j] : 0.0;
+        }
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            const int j = i + u * g.nt;
+            if (j < i1) dst[j] = x[u];
+        }
+    }
+}
+
+// L2 prefetch hint for the 16-byte-aligned part of [p, p + bytes) (one bulk
+// instruction; never touches bytes outside the range).
+__device__ __forceinline__ void prefetch_l2(const void* p, size_t bytes) {
+    const unsigned long long a = ((unsigned long long)p + 15ull) & ~15ull;
+    const unsigned long long e = ((unsigned long long)p + bytes) & ~15ull;
+    if (e > a)
+        asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(a), "r"((unsigned)(e - a)) : "memory");
+}
+
+// lv[l] += dL/dv at the group's probes (row of dLdv): probes [q0, q1) are
+// sorted by node, so each node's run is summed in probe order by one thread.
+__device__ __forceinline__ void probe_inject(const DevProbe& P, int q0, int q1, const double* __restrict__ row,
+                                             double* lv, const Grp& g) {
+    for (int q = q0 + g.tl; q < q1; q += g.nt) {
+        const int l = P.local[q];
+        if (q > q0 && P.local[q - 1] == l) continue;
+        double s = lv[l];
+        for (int r = q; r < q1 && P.local[r] == l; ++r) s += row[P.slot[r]];
+        lv[l] = s;
+    }
+    __threadfence_block();
 }
 
 // ------------------------------------------------------------------ assembly
