@@ -97,6 +97,8 @@ class PlanStats(C.Structure):
         ("smem_fwd", C.c_size_t),
         ("smem_bwd", C.c_size_t),
         ("nsub", C.c_int),
+        ("est_max", C.c_double),
+        ("est_mean", C.c_double),
     ]
 
     def as_dict(self):
@@ -116,6 +118,7 @@ SIGNATURES = {
     "hx_get_plan_stats": (C.c_int, [C.c_void_p, C.POINTER(PlanStats)]),
     "hx_plan_check": (C.c_int, [C.POINTER(GroupDesc), C.c_int, C.POINTER(PlanStats), _dp, _dp]),
     "hx_plan_check_cap": (C.c_int, [C.POINTER(GroupDesc), C.c_int, C.c_int, C.POINTER(PlanStats), _dp, _dp]),
+    "hx_plan_check_sm": (C.c_int, [C.POINTER(GroupDesc), C.c_int, C.c_int, C.c_int, C.POINTER(PlanStats), _dp, _dp]),
     "hx_set_param": (C.c_int, [C.c_void_p, C.c_int, _dp, C.c_int]),
     "hx_get_param": (C.c_int, [C.c_void_p, C.c_int, _dp, C.c_int]),
     "hx_simulate": (C.c_int, [C.c_void_p, C.c_int, C.c_double, C.c_int, _ip, _dp]),
@@ -258,15 +261,17 @@ def netstim_trains(g, nstep: int):
     return ids[:cap], steps[:cap]
 
 
-def plan_check(g, nodes_per_pack: int = 0, max_pack_nodes: int = 0):
-    """Host-only plan build + CPU check of the planned Hines order (no GPU needed)."""
+def plan_check(g, nodes_per_pack: int = 0, max_pack_nodes: int = 0, nsm: int = 0):
+    """Host-only plan build + CPU check of the planned Hines order (no GPU needed).
+
+    nsm > 0 plans for a device of that many SMs (CTAs balanced over waves)."""
     L = load()
     b = BoundGroup(g)
     st = PlanStats()
     diff = C.c_double(-1.0)
     pq = C.c_double(-1.0)
-    rc = L.hx_plan_check_cap(C.byref(b.desc), int(nodes_per_pack), int(max_pack_nodes), C.byref(st), C.byref(diff),
-                             C.byref(pq))
+    rc = L.hx_plan_check_sm(C.byref(b.desc), int(nodes_per_pack), int(max_pack_nodes), int(nsm), C.byref(st),
+                            C.byref(diff), C.byref(pq))
     if rc != 0:
         raise ValueError(f"hx_plan_check failed (rc={rc})")
     d = st.as_dict()

@@ -5,7 +5,9 @@
 #include <cmath>
 #include <cstdint>
 #include <numeric>
+#include <map>
 #include <queue>
+#include <random>
 #include <set>
 #include <sstream>
 #include <unordered_map>
@@ -329,41 +331,114 @@ std::string build_plan(const hx_group_desc& g, int nodes_per_warp, int max_pack_
             bin_n[b] += usize[c];
         }
     }
-    for (size_t b = 0; b < bins.size(); b++) {
-        const int nb = (int)bins[b].size();
-        const double tot = (double)bin_n[b];
-        int used = 0;
-        std::vector<std::pair<double, int>> rem;
-        for (int c : bins[b]) {
-            const double share = kWarpsPerCta * (double)usize[c] / tot;
-            wc[c] = std::max(1, (int)std::floor(share));
-            used += wc[c];
-            rem.push_back({share - std::floor(share), c});
+    // Warps per cell and (balanced mode) the choice of cells per CTA follow an
+    // estimate of a cell's forward + backward step time with w warps: the
+    // latency of its Hines sweeps -- per node of the level-by-level critical
+    // path (sum over levels of the longest branch) and per level -- plus the
+    // per-node loops, whose time goes with the nodes each thread carries.  The
+    // constants are cycles measured on B200 for the hh + pas kernels; only
+    // their ratios matter.  A CTA finishes with its slowest cell, so warps go
+    // one at a time to the cell with the largest estimate, and in balanced
+    // mode cells are moved / swapped out of the slowest CTA while that lowers
+    // its estimate.
+    constexpr double kHinesNode = 260.0, kHinesLevel = 4100.0, kNodeIter = 14200.0;
+    std::vector<double> uh(nunit, 0.0);
+    for (int u = 0; u < nunit; u++) {
+        std::map<int, int> longest;
+        for (const Branch& br : ubr[u]) {
+            int& l = longest[br.level];
+            l = std::max(l, (int)br.nodes.size());
         }
-        // hand out the rest by largest remainder (then most nodes per warp)
-        std::stable_sort(rem.begin(), rem.end(), [&](const std::pair<double, int>& x, const std::pair<double, int>& y) {
-            return x.first > y.first;
-        });
-        for (size_t i = 0; used < kWarpsPerCta && nb > 0; i = (i + 1) % rem.size()) {
-            wc[rem[i].second]++;
-            used++;
-        }
-        // floor-at-one may have overshot for packs of many small cells: take warps
-        // back from the cells with the fewest nodes per warp
-        while (used > kWarpsPerCta) {
+        double crit = 0.0;
+        for (auto& kv : longest) crit += kv.second;
+        uh[u] = kHinesNode * crit + kHinesLevel * (double)longest.size();
+    }
+    auto unit_time = [&](int u, int w) {
+        return uh[u] + kNodeIter * std::ceil((double)usize[u] / (32.0 * (double)w));
+    };
+    // greedy warps of one CTA; returns the CTA's estimate
+    auto assign_warps = [&](const std::vector<int>& cs, std::vector<int>& w) {
+        for (int c : cs) w[c] = 1;
+        int used = (int)cs.size();
+        while (used < kWarpsPerCta && !cs.empty()) {
             int best = -1;
-            double bv = 1e300;
-            for (int c : bins[b]) {
-                double v = (double)usize[c] / wc[c];
-                if (wc[c] > 1 && v < bv) {
-                    bv = v;
+            double bt = -1.0;
+            for (int c : cs) {
+                const double t = unit_time(c, w[c]);
+                if (t > bt && unit_time(c, w[c] + 1) < t) {
+                    bt = t;
                     best = c;
                 }
             }
-            if (best < 0) break;
-            wc[best]--;
-            used--;
+            if (best < 0) {  // no cell gets faster: spread the rest by nodes per warp
+                for (int c : cs)
+                    if (best < 0 || (double)usize[c] / w[c] > (double)usize[best] / w[best]) best = c;
+            }
+            w[best]++;
+            used++;
         }
+        double t = 0.0;
+        for (int c : cs) t = std::max(t, unit_time(c, w[c]));
+        return t;
+    };
+    if (balanced && (int)bins.size() > b0 + 1) {
+        std::vector<int> wtmp(nunit, 1);
+        std::vector<double> bt(bins.size(), 0.0);
+        for (size_t k = b0; k < bins.size(); k++) bt[k] = assign_warps(bins[k], wtmp);
+        std::mt19937 rng(20240611u);
+        const int nbin = (int)bins.size() - b0;
+        const int iters = std::min(60000, 4000 + 40 * nbin);
+        for (int it = 0; it < iters; it++) {
+            int a = b0;
+            for (int k = b0; k < (int)bins.size(); k++)
+                if (bt[k] > bt[a]) a = k;
+            const int o = b0 + (int)(rng() % (unsigned)nbin);
+            if (o == a || bins[a].empty()) continue;
+            const int ia = (int)(rng() % bins[a].size());
+            const int ca = bins[a][ia];
+            std::vector<int> na = bins[a], no = bins[o];
+            int dn_a = -usize[ca], dn_o = usize[ca];
+            na.erase(na.begin() + ia);
+            const bool move = (rng() & 1) || bins[o].empty();
+            if (move) {
+                if (na.empty() || (int)no.size() >= kWarpsPerCta) continue;
+                no.push_back(ca);
+            } else {
+                const int io = (int)(rng() % bins[o].size());
+                const int co = bins[o][io];
+                no.erase(no.begin() + io);
+                no.push_back(ca);
+                na.push_back(co);
+                dn_a += usize[co];
+                dn_o -= usize[co];
+            }
+            if (bin_n[a] + dn_a > cap || bin_n[o] + dn_o > cap) continue;
+            const double ta = assign_warps(na, wtmp), to = assign_warps(no, wtmp);
+            if (std::max(ta, to) < bt[a]) {
+                bins[a].swap(na);
+                bins[o].swap(no);
+                bin_n[a] += dn_a;
+                bin_n[o] += dn_o;
+                bt[a] = ta;
+                bt[o] = to;
+            }
+        }
+        std::vector<std::vector<int>> kept;
+        std::vector<int> kept_n;
+        for (size_t k = 0; k < bins.size(); k++)
+            if (!bins[k].empty()) {
+                kept.push_back(std::move(bins[k]));
+                kept_n.push_back(bin_n[k]);
+            }
+        bins.swap(kept);
+        bin_n.swap(kept_n);
+    }
+    P.est_max = 0.0;
+    P.est_mean = 0.0;
+    for (size_t b = 0; b < bins.size(); b++) {
+        const double t = assign_warps(bins[b], wc);
+        P.est_max = std::max(P.est_max, t);
+        P.est_mean += t / (double)bins.size();
         std::sort(bins[b].begin(), bins[b].end());
     }
     const int npack = (int)bins.size();

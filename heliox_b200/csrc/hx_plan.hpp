@@ -67,6 +67,7 @@ struct Plan {
     int max_pack_nodes = 0, max_pack_hh = 0, max_levels = 0, max_crit = 0;
     int max_pack_branches = 0, max_pack_bch = 0, max_pack_nch = 0;
     double imbalance = 1.0;
+    double est_max = 0.0, est_mean = 0.0;  // modelled cycles of one forward + backward step: slowest / mean CTA
 };
 
 // Validates the group and builds the plan.  nodes_per_warp: target cell nodes

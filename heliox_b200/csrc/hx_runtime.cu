@@ -94,13 +94,17 @@ static int store_kind(int kind) {
 double* hx_kind_ptr(hx_ctx* c, int kind) { return c->prm[store_kind(kind)].p; }
 size_t hx_grad_base(const hx_ctx* c, int kind) { return c->grad_off[store_kind(kind)]; }
 
-// dynamic shared memory per CTA of the two step kernels for a plan
+// dynamic shared memory per CTA of the two step kernels for a plan (the
+// split-cell kernels when the plan splits a cell)
 static void plan_smem(const hx::Plan& P, size_t& fwd, size_t& bwd) {
-    const size_t n = std::max(P.max_pack_nodes, 1);
-    const size_t lvl = (size_t)hx::kWarpsPerCta * (P.max_levels + 1);
-    const size_t ints = 3 * n + 1 + P.max_pack_nch + 4 * (size_t)P.max_pack_branches + 1 + P.max_pack_bch + lvl;
-    fwd = 8 * n * sizeof(double) + ints * sizeof(int);
-    bwd = 10 * n * sizeof(double) + ints * sizeof(int);
+    hx::DevGroup Gt{};
+    Gt.smem_n = std::max(P.max_pack_nodes, 1);
+    Gt.smem_br = P.max_pack_branches;
+    Gt.smem_bch = P.max_pack_bch;
+    Gt.smem_nch = P.max_pack_nch;
+    Gt.smem_lvl = hx::kWarpsPerCta * (P.max_levels + 1);
+    fwd = P.nsub > 0 ? hx::split_fwd_smem_bytes(Gt) : hx::fwd_smem_bytes(Gt);
+    bwd = P.nsub > 0 ? hx::split_bwd_smem_bytes(Gt) : hx::bwd_smem_bytes(Gt);
 }
 
 static void fill_stats(const hx::Plan& P, hx_plan_stats* out) {
@@ -112,6 +116,8 @@ static void fill_stats(const hx::Plan& P, hx_plan_stats* out) {
     out->nbranch = (int)P.br_head.size();
     out->imbalance = P.imbalance;
     out->nsub = P.nsub;
+    out->est_max = P.est_max;
+    out->est_mean = P.est_mean;
     plan_smem(P, out->smem_fwd, out->smem_bwd);
 }
 
@@ -183,9 +189,14 @@ int hx_plan_check(const hx_group_desc* desc, int nodes_per_warp, hx_plan_stats* 
 
 int hx_plan_check_cap(const hx_group_desc* desc, int nodes_per_warp, int max_pack_nodes, hx_plan_stats* out,
                       double* max_abs_diff, double* pq_rel_diff) {
+    return hx_plan_check_sm(desc, nodes_per_warp, max_pack_nodes, 0, out, max_abs_diff, pq_rel_diff);
+}
+
+int hx_plan_check_sm(const hx_group_desc* desc, int nodes_per_warp, int max_pack_nodes, int nsm, hx_plan_stats* out,
+                     double* max_abs_diff, double* pq_rel_diff) {
     if (!desc) return -1;
     hx::Plan P;
-    std::string e = hx::build_plan(*desc, nodes_per_warp, max_pack_nodes, P);
+    std::string e = hx::build_plan(*desc, nodes_per_warp, max_pack_nodes, P, nsm);
     if (!e.empty()) {
         fprintf(stderr, "hx_plan_check: %s\n", e.c_str());
         return -2;

@@ -115,6 +115,8 @@ typedef struct hx_plan_stats {
     double imbalance;     /* max pack nodes / mean pack nodes */
     size_t smem_fwd, smem_bwd; /* dynamic shared memory per CTA (bytes) */
     int nsub;             /* subtrees of a cell split across CTAs (0: no split) */
+    double est_max;       /* modelled cycles of a forward + backward step: slowest CTA */
+    double est_mean;      /* the same, mean over CTAs */
 } hx_plan_stats;
 
 /* ---- context ------------------------------------------------------------ */
@@ -154,6 +156,10 @@ int hx_plan_check(const hx_group_desc* desc, int nodes_per_warp, hx_plan_stats* 
  * each, as hx_load_group does when a cell exceeds a CTA's shared memory. */
 int hx_plan_check_cap(const hx_group_desc* desc, int nodes_per_warp, int max_pack_nodes, hx_plan_stats* out,
                       double* max_abs_diff, double* pq_rel_diff);
+/* The same for a device of nsm SMs: with nodes_per_warp = 0 the CTAs are
+ * balanced over whole waves of nsm CTAs, as hx_load_group plans them. */
+int hx_plan_check_sm(const hx_group_desc* desc, int nodes_per_warp, int max_pack_nodes, int nsm, hx_plan_stats* out,
+                     double* max_abs_diff, double* pq_rel_diff);
 
 /* Parameter access in reference instance order (replaces the handle-based
  * Sim.set/get_variable path, src/python_api/PyBindings.cpp:80-81). */
