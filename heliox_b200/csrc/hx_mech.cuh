@@ -10,7 +10,7 @@
 // exponential z = exp(-(v+65)/720) times constants:
 //   exp(-(v+65)/18) = z^40, exp(-(v+65)/20) = z^36, exp(-(v+65)/80) = z^9,
 //   exp(-(v+40)/10) = z^72 e^2.5, exp(-(v+55)/10) = z^72 e, exp(-(v+35)/10) = z^72 e^3,
-// and quotients by positive sums use a Newton reciprocal.  These forms equal
+// and quotients use a Newton reciprocal.  These forms equal
 // the reference's mathematically and differ by rounding only (a few 1e-14
 // relative in the rates); parity is checked against the reference-order CPU
 // oracle.
@@ -25,10 +25,10 @@ namespace hx {
 constexpr double kFdEps = 0.001;  // mech_template.cuh:616 and :626
 constexpr double kInvFdEps = 1000.0;
 
-// Branch-free reciprocal for positive normal x: hardware estimate refined by
-// two Newton-Raphson steps r <- r + r*(1 - x*r) (quadratic convergence from the
-// ~2^-23 estimate to below double rounding).
-__device__ __forceinline__ double rcp_pos(double x) {
+// Branch-free reciprocal of a nonzero normal x (either sign): hardware
+// estimate refined by two Newton-Raphson steps r <- r + r*(1 - x*r) (quadratic
+// convergence from the ~2^-23 estimate to below double rounding).
+__device__ __forceinline__ double rcp_nz(double x) {
     double r;
     asm("rcp.approx.ftz.f64 %0, %1;" : "=d"(r) : "d"(x));
     double e = __fma_rn(-x, r, 1.0);
@@ -65,7 +65,7 @@ __device__ __forceinline__ ZPow zpow(double v) {
 __device__ __forceinline__ double vtrap10_e(double x, double ex) {
     const double u = x * 0.1;
     if (fabs(u) < 1e-6) return 10.0 * (1 - u * 0.5);
-    return x / (ex - 1);
+    return x * rcp_nz(ex - 1);
 }
 
 __device__ __forceinline__ void hh_rates(double v, double q10, HHRates& r) {
@@ -74,17 +74,17 @@ __device__ __forceinline__ void hh_rates(double v, double q10, HHRates& r) {
     al = 0.1 * vtrap10_e(-(v + 40), Z.z72 * kE25);
     be = 4 * Z.z40;
     s = al + be;
-    r.inf[0] = al * rcp_pos(s);
+    r.inf[0] = al * rcp_nz(s);
     r.k[0] = q10 * s;
     al = 0.07 * Z.z36;
-    be = rcp_pos(Z.z72 * kE3 + 1);
+    be = rcp_nz(Z.z72 * kE3 + 1);
     s = al + be;
-    r.inf[1] = al * rcp_pos(s);
+    r.inf[1] = al * rcp_nz(s);
     r.k[1] = q10 * s;
     al = 0.01 * vtrap10_e(-(v + 55), Z.z72 * kE1);
     be = 0.125 * Z.z9;
     s = al + be;
-    r.inf[2] = al * rcp_pos(s);
+    r.inf[2] = al * rcp_nz(s);
     r.k[2] = q10 * s;
 }
 
@@ -96,7 +96,7 @@ __device__ __forceinline__ void vtrap10_d_e(double x, double ex, double& f, doub
         df = -0.5;
     } else {
         const double em1 = ex - 1;
-        const double r = 1.0 / em1;
+        const double r = rcp_nz(em1);
         f = x * r;
         df = (em1 - u * ex) * (r * r);
     }
@@ -116,7 +116,7 @@ __device__ __forceinline__ void hh_rates_d(double v, double q10, HHRatesD& r) {
     be = 4 * Z.z40;
     dbe = be * (-1.0 / 18);
     s = al + be;
-    rs = rcp_pos(s);
+    rs = rcp_nz(s);
     r.inf[0] = al * rs;
     r.k[0] = q10 * s;
     r.dinf[0] = (dal * be - al * dbe) * (rs * rs);
@@ -125,11 +125,11 @@ __device__ __forceinline__ void hh_rates_d(double v, double q10, HHRatesD& r) {
     dal = al * (-1.0 / 20);
     {
         const double u = Z.z72 * kE3;
-        be = rcp_pos(u + 1);
+        be = rcp_nz(u + 1);
         dbe = u * 0.1 * (be * be);
     }
     s = al + be;
-    rs = rcp_pos(s);
+    rs = rcp_nz(s);
     r.inf[1] = al * rs;
     r.k[1] = q10 * s;
     r.dinf[1] = (dal * be - al * dbe) * (rs * rs);
@@ -140,7 +140,7 @@ __device__ __forceinline__ void hh_rates_d(double v, double q10, HHRatesD& r) {
     be = 0.125 * Z.z9;
     dbe = be * (-1.0 / 80);
     s = al + be;
-    rs = rcp_pos(s);
+    rs = rcp_nz(s);
     r.inf[2] = al * rs;
     r.k[2] = q10 * s;
     r.dinf[2] = (dal * be - al * dbe) * (rs * rs);

@@ -134,7 +134,7 @@ __device__ __forceinline__ void tri_split(const DevGroup& G, const Meta& M, cons
                 yy *= s;
             }
             if (j > h) tri_block<true>(d, rhs, A, U, j, j - h, pp, qq, yy);
-            const double ip = rcp_pos(pp);
+            const double ip = rcp_nz(pp);
             d[h] = qq * ip;
             rhs[h] = yy * ip;
         }

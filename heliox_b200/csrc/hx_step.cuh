@@ -73,7 +73,7 @@ __device__ __forceinline__ void tri_block(double* __restrict__ d, double* __rest
 #pragma unroll
     for (int u = 0; u < kBlk; ++u) {
         if (!kGuard || u < cnt) {
-            const double ip = rcp_pos(pv[u]);
+            const double ip = rcp_nz(pv[u]);
             d[j - u] = qv[u] * ip;
             rhs[j - u] = yv[u] * ip;
         }
@@ -230,7 +230,7 @@ __device__ __forceinline__ void hines_cell(const Meta& M, const Grp& g, const do
                 yy *= s;
             }
             if (j > h) tri_block<true>(d, rhs, A, U, j, j - h, pp, qq, yy);
-            const double ip = rcp_pos(pp);
+            const double ip = rcp_nz(pp);
             d[h] = qq * ip;
             rhs[h] = yy * ip;
         }
