@@ -103,9 +103,11 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_kernel(DevGroup G, DevState S
     if (k0 == 0 && trace)
         for (int q = q0 + g.tl; q < q1; q += g.nt) trace[P.slot[q]] = sv[P.local[q]];
     for (int k = k0; k < k1; ++k) {
+        // tape rows are written with streaming stores (evict first) so that the
+        // row stream does not push the per-node parameters out of L2
         const size_t toff = (size_t)(k - T.k_base) * (size_t)G.nnode + pb;
         if (write_tape)
-            for (int i = i0 + g.tl; i < i1; i += g.nt) T.v[toff + i] = sv[i];
+            for (int i = i0 + g.tl; i < i1; i += g.nt) __stcs(T.v + toff + i, sv[i]);
         if (kNet) {
             if (N.detect && g.tl == 0 && psnode >= 0) {
                 const double pv = sv[psnode];
@@ -163,9 +165,9 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_kernel(DevGroup G, DevState S
                 S.n[pb + i] = gn;
             }
             if (write_tape && (fl & kHasHH)) {
-                T.m[toff + i] = gm;
-                T.h[toff + i] = gh;
-                T.n[toff + i] = gn;
+                __stcs(T.m + toff + i, gm);
+                __stcs(T.h + toff + i, gh);
+                __stcs(T.n + toff + i, gn);
             }
             double r, dd;
             if (kNet) {
@@ -214,7 +216,7 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_kernel(DevGroup G, DevState S
     }
     if (write_tape) {
         const size_t off = (size_t)(k1 - T.k_base) * (size_t)G.nnode + pb;
-        for (int i = i0 + g.tl; i < i1; i += g.nt) T.v[off + i] = sv[i];
+        for (int i = i0 + g.tl; i < i1; i += g.nt) __stcs(T.v + off + i, sv[i]);
     }
     double* vdst = (kNet && N.coupled) ? N.vout : S.v;
     for (int i = i0 + g.tl; i < i1; i += g.nt) {
@@ -374,7 +376,9 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_kernel(DevGroup G, DevTape T,
             load_par(G, gi, fl, q);
             const double w = sw[i];
             const double vk = T.v[off + i];
-            const double ld = -w * (T.v[off + G.nnode + i] - vk);
+            // last read of row k+1 (streaming load); rows are read twice, once as
+            // row k of their own step and once as row k+1 of the step below
+            const double ld = -w * (__ldcs(T.v + off + G.nnode + i) - vk);
             const double lvn0 = lv[i];
             double lm = 0.0, lh = 0.0, ln = 0.0;
             if (fl & kHasHH) {

@@ -390,9 +390,10 @@ __device__ __forceinline__ double vjp_mech(const DevGroup& G, const DevGrad& GR,
         a_pe = GR.pas_e[gi];
     }
     if (fl & kHasHH) {
-        m = T.m[off + i];
-        h = T.h[off + i];
-        nn = T.n[off + i];
+        // the gates' last read of their tape row (streaming loads)
+        m = __ldcs(T.m + off + i);
+        h = __ldcs(T.h + off + i);
+        nn = __ldcs(T.n + off + i);
         a_na = GR.hh_gnabar[gi];
         a_k = GR.hh_gkbar[gi];
         a_l = GR.hh_gl[gi];
