@@ -327,24 +327,14 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_kernel(DevGroup G, DevTape T,
             const double vk = T.v[off + i];
             double gm = 0.0, gh = 0.0, gn = 0.0;
             if (fl & kHasHH) {
-                const double v1 = T.v[off + G.nnode + i];
                 gm = T.m[off + i];
                 gh = T.h[off + i];
                 gn = T.n[off + i];
-                double lam[3] = {lmv[i], lhv[i], lnv[i]};
-                HHRatesD R;
-                hh_rates_d(v1, q10, R);
-                const double x[3] = {gm, gh, gn};
-#pragma unroll
-                for (int q = 0; q < 3; ++q) {
-                    const double E = exp(-dt * R.k[q]);
-                    const double dnew = (1.0 - E) * R.dinf[q] + (R.inf[q] - x[q]) * E * dt * q10 * R.ds[q];
-                    mu += lam[q] * dnew;
-                    lam[q] *= E;
-                }
-                lmv[i] = lam[0];
-                lhv[i] = lam[1];
-                lnv[i] = lam[2];
+                double lm = lmv[i], lh = lhv[i], ln = lnv[i];
+                mu = gate_adj(T.v[off + G.nnode + i], q10, dt, gm, gh, gn, mu, lm, lh, ln);
+                lmv[i] = lm;
+                lhv[i] = lh;
+                lnv[i] = ln;
             }
             // (parameters loaded after the rate chain: held across it they spill)
             NodePar q;

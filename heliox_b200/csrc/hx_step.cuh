@@ -375,6 +375,28 @@ __device__ __forceinline__ void load_par(const DevGroup& G, int gi, int fl, Node
     q.ic1 = __ldg(G.node_ic_off + gi + 1);
 }
 
+// Adjoint of the gates' cnexp update gates_{k+1} = E gates_k + (1 - E) inf(v_{k+1}),
+// E = exp(-dt k(v_{k+1})) (hh_templated.cu:151-164): returns mu plus the gates'
+// v_{k+1}-derivatives weighted by their adjoints, and scales the adjoints by E.
+__device__ __forceinline__ double gate_adj(double v1, double q10, double dt, double gm, double gh, double gn,
+                                           double mu, double& lm, double& lh, double& ln) {
+    HHRatesD R;
+    hh_rates_d(v1, q10, R);
+    const double x[3] = {gm, gh, gn};
+    double lam[3] = {lm, lh, ln};
+#pragma unroll
+    for (int q = 0; q < 3; ++q) {
+        const double E = exp(-dt * R.k[q]);
+        const double dnew = (1.0 - E) * R.dinf[q] + (R.inf[q] - x[q]) * E * dt * q10 * R.ds[q];
+        mu += lam[q] * dnew;
+        lam[q] *= E;
+    }
+    lm = lam[0];
+    lh = lam[1];
+    ln = lam[2];
+    return mu;
+}
+
 // Mechanism part of the VJP of step k at GPU node gi (pas, hh, IClamp,
 // capacitance): w = (M^-T mu)_i, ld = -w (v_{k+1} - v_k).  Accumulates the
 // parameter gradients, adds the gate adjoint increments to lm/lh/ln and
