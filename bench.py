@@ -45,9 +45,11 @@ T_STEPS = 4000
 NCELL = 1024
 SEED0 = 20240
 # DRAM bytes per compartment-step of the backward kernel from the committed ncu
-# capture (profiles/fwd_bwd_kernels_config2_small.md: dram__bytes_read.sum +
-# dram__bytes_write.sum over the captured launch / its compartment-steps).
-BWD_DRAM_BYTES_PER_UNIT = 34.6
+# capture (profiles/fwd_bwd_kernels_config2_100steps.md: dram__bytes_read.sum +
+# dram__bytes_write.sum of the captured launch / its compartment-steps; the
+# capture runs the config-2 cells for 100 steps, and the per-step traffic does
+# not depend on the step count).
+BWD_DRAM_BYTES_PER_UNIT = 349.0
 
 
 def _alg_bytes(g):

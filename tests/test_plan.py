@@ -79,7 +79,7 @@ def test_packing_balance_and_coverage():
     g = synth.random_tree_batch(96, seed0=3)
     stats, diff = _lib.plan_check(g, 0)
     assert diff == 0.0
-    # packs hold whole cells in 8-warp CTAs; node counts stay within 1.6x of the mean
+    # packs hold whole cells in 16-warp CTAs; node counts stay within 1.6x of the mean
     assert stats["imbalance"] < 1.6
     assert stats["nbranch"] >= g.ncell
     assert stats["max_pack_nodes"] >= 1000 or stats["npack"] == 1
@@ -92,3 +92,31 @@ def test_invalid_group_rejected():
     bad.parent[5] = 7  # parent after child
     with pytest.raises(ValueError):
         _lib.plan_check(bad)
+
+
+@pytest.mark.parametrize("ncell,cap,nsm", [(296, 4500, 148), (1024, 4500, 148), (700, 2000, 64), (40, 4500, 148)])
+def test_balanced_packing_over_sms(ncell, cap, nsm):
+    """Device-aware plan (hx_load_group's default): whole cells dealt over
+    whole waves of nsm CTAs within the node capacity, warps by the step-time
+    model; the planned solve stays bit-exact."""
+    g = synth.random_tree_batch(ncell, seed0=101)
+    stats, diff = _lib.plan_check(g, 0, cap, nsm)
+    assert diff == 0.0
+    assert stats["pq_rel_diff"] <= 1e-13
+    assert stats["max_pack_nodes"] <= cap
+    total = g.nnode
+    waves = -(-total // (nsm * int(cap * 0.96)))
+    assert stats["npack"] <= max(waves * nsm, -(-ncell // 16))
+    assert stats["npack"] >= min(ncell, nsm) or stats["npack"] * cap >= total
+    assert stats["est_mean"] > 0
+    if ncell >= 2 * nsm:  # several cells a CTA: the slowest CTA's modelled step time stays near the mean
+        assert stats["est_max"] <= 1.35 * stats["est_mean"]
+    if ncell <= nsm:  # fewer cells than SMs: one cell a CTA
+        assert stats["npack"] == ncell
+
+
+def test_balanced_plan_is_deterministic():
+    g = synth.random_tree_batch(300, seed0=5)
+    a, _ = _lib.plan_check(g, 0, 4000, 148)
+    b, _ = _lib.plan_check(g, 0, 4000, 148)
+    assert a == b
