@@ -343,8 +343,18 @@ def run_ours(args):
     _, nb = s.last_kernel_ms(1)
     gpu_launches = args.steps * (1 + nf + 2 + nb + len(keys))
 
-    # ---- end to end through the public host-buffer API (params in, loss/grads out)
-    host_params = {k: np.ascontiguousarray(s.get_param_array(k)) for k in keys}
+    # ---- end to end through the public host-buffer API (params in, loss/grads out),
+    # host buffers page-locked (inputs from pinned host memory, results read
+    # into pinned memory), allocated once outside the timed region
+    from heliox_b200.runtime import pinned_empty
+
+    host_params = {}
+    for k in keys:
+        host_params[k] = pinned_empty(counts[k])
+        host_params[k][:] = s.get_param_array(k)
+    tr_h = pinned_empty((T + 1, nprobe))
+    dl_h = pinned_empty((T + 1, nprobe))
+    grads_h = {k: pinned_empty(counts[k]) for k in keys}
     if not (ws > 1 and W.get("exchange")):  # the exchange hook runs on torch's stream
         s.set_stream(0)
     torch.cuda.synchronize()
@@ -357,11 +367,11 @@ def run_ours(args):
     for _ in range(e2e_steps):
         for k in keys:
             s.set_param_array(k, host_params[k])
-        tr = s.forward_capture(T, probes=probes)
-        err = tr - target_h
-        dl = (2.0 / (T * nprobe)) * err
-        dl[0] = 0.0
-        gg = s.backward(dl, keys=keys)
+        s.forward_capture(T, probes=probes, out=tr_h)
+        np.subtract(tr_h, target_h, out=dl_h)
+        dl_h *= 2.0 / (T * nprobe)
+        dl_h[0] = 0.0
+        s.backward(dl_h, keys=keys, out=grads_h)
     e2e_s = (time.perf_counter() - t0) * args.steps / e2e_steps
     if dist:
         dist.barrier()

@@ -523,11 +523,20 @@ int hx_set_param(hx_ctx* ctx, int kind, const double* values, int n) {
     if ((size_t)n != cnt) return fail(ctx, "parameter count mismatch");
     if (!cnt) return 0;
     HXC(cudaSetDevice(ctx->device));
-    HXC(ctx->pin.ensure(cnt * sizeof(double)));
-    HXC(cudaStreamSynchronize(ctx->st));  // the pinned staging buffer may still be in flight
-    memcpy(ctx->pin.p, values, cnt * sizeof(double));
+    // page-locked caller memory is copied directly; other memory goes through
+    // the runtime's pinned staging buffer
+    cudaPointerAttributes pa{};
+    const bool pinned = cudaPointerGetAttributes(&pa, values) == cudaSuccess && pa.type == cudaMemoryTypeHost;
+    if (!pinned) (void)cudaGetLastError();
+    const double* src = values;
+    if (!pinned) {
+        HXC(ctx->pin.ensure(cnt * sizeof(double)));
+        HXC(cudaStreamSynchronize(ctx->st));  // the pinned staging buffer may still be in flight
+        memcpy(ctx->pin.p, values, cnt * sizeof(double));
+        src = static_cast<const double*>(ctx->pin.p);
+    }
     double* stage = ctx->stage_dev.p;
-    HXC(cudaMemcpyAsync(stage, ctx->pin.p, cnt * sizeof(double), cudaMemcpyHostToDevice, ctx->st));
+    HXC(cudaMemcpyAsync(stage, src, cnt * sizeof(double), cudaMemcpyHostToDevice, ctx->st));
     HXC(hx::launch_scatter(stage, ctx->kmap[kind].p, hx_kind_ptr(ctx, kind), (int)cnt, ctx->st));
     HXC(cudaStreamSynchronize(ctx->st));
     return 0;

@@ -52,6 +52,24 @@ class HxError(RuntimeError):
     pass
 
 
+def pinned_empty(shape, dtype=np.float64) -> np.ndarray:
+    """Uninitialised page-locked host array (host<->device copies at full link
+    rate and without first-touch page faults); torch provides the allocation."""
+    import torch
+
+    shape = (int(shape),) if np.isscalar(shape) else tuple(int(x) for x in shape)
+    t = torch.empty(shape, dtype=torch.from_numpy(np.zeros(0, dtype=dtype)).dtype, pin_memory=True)
+    return t.numpy()  # the array keeps the tensor (its base) alive
+
+
+def _out_array(out: Optional[np.ndarray], shape) -> np.ndarray:
+    if out is None:
+        return np.zeros(shape)
+    if out.dtype != np.float64 or out.shape != tuple(shape) or not out.flags["C_CONTIGUOUS"] or not out.flags["WRITEABLE"]:
+        raise ValueError(f"out must be a writeable C-contiguous float64 array of shape {tuple(shape)}")
+    return out
+
+
 class Sim:
     """One simulation/learning runtime bound to one CUDA device."""
 
@@ -218,10 +236,15 @@ class Sim:
                     "hx_simulate")
         return tr
 
-    def forward_capture(self, nstep: int, v_init: Optional[float] = None, probes=None) -> np.ndarray:
-        """Forward that records the tape for ``backward``; returns the probe trace."""
+    def forward_capture(self, nstep: int, v_init: Optional[float] = None, probes=None,
+                        out: Optional[np.ndarray] = None) -> np.ndarray:
+        """Forward that records the tape for ``backward``; returns the probe trace.
+
+        ``out``: optional C-contiguous float64 array of shape (nstep+1, nprobe)
+        to write the trace into (e.g. from ``pinned_empty``, for full-rate
+        copies); otherwise a new array is returned."""
         p = self._probe_arr(probes)
-        tr = np.zeros((nstep + 1, p.shape[0]))
+        tr = _out_array(out, (nstep + 1, p.shape[0]))
         vi = self.group.v_init if v_init is None else v_init
         self._check(
             self._L.hx_forward_capture(self._ctx, int(nstep), float(vi), int(p.shape[0]), _lib.iptr(p), _lib.dptr(tr)),
@@ -230,14 +253,19 @@ class Sim:
         return tr
 
     # ------------------------------------------------------------------ backward
-    def backward(self, dLdv: np.ndarray, keys: Iterable[str] = tuple(_lib.HX_P)) -> Dict[str, np.ndarray]:
-        """Exact adjoint of the last capture; dLdv shape (nstep+1, nprobe)."""
+    def backward(self, dLdv: np.ndarray, keys: Iterable[str] = tuple(_lib.HX_P),
+                 out: Optional[Dict[str, np.ndarray]] = None) -> Dict[str, np.ndarray]:
+        """Exact adjoint of the last capture; dLdv shape (nstep+1, nprobe).
+
+        ``out``: optional dict of C-contiguous float64 arrays (one per key, of
+        the parameter's instance count) to write the gradients into."""
         if self._nstep is None:
             raise HxError("backward needs a preceding forward_capture")
         d = np.ascontiguousarray(dLdv, dtype=np.float64)
         if d.shape != (self._nstep + 1, self._probes.shape[0]):
             raise ValueError(f"dLdv must have shape {(self._nstep + 1, self._probes.shape[0])}")
-        outs = {k: np.zeros(self._count(k)) for k in keys}
+        out = out or {}
+        outs = {k: _out_array(out.get(k), (self._count(k),)) for k in keys}
         arr = (_lib._dp * _lib.HX_P_COUNT)()
         for k, v in outs.items():
             arr[_lib.HX_P[k]] = _lib.dptr(v)
