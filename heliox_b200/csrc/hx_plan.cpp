@@ -703,7 +703,7 @@ void planned_solve_pq_cpu(const Plan& P, const double* a, const double* b, doubl
             double pp = de, qq = 1.0, yy = re;
             for (int j = e; j > h; j--) {
                 const double pn = std::fma(d[j - 1], pp, -((A[j] * U[j]) * qq));
-                const double yn = std::fma(rhs[j - 1], pp, -(A[j] * yy));
+                const double yn = std::fma(-A[j], yy, rhs[j - 1] * pp);
                 const double ip = 1.0 / pp;
                 d[j] = qq * ip;
                 rhs[j] = yy * ip;

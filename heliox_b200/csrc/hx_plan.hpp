@@ -82,8 +82,9 @@ std::string build_plan(const hx_group_desc& g, int nodes_per_warp, int max_pack_
 void planned_solve_cpu(const Plan& P, const double* a, const double* b, double* d, double* rhs, bool transposed);
 
 // CPU emulation of the kernels' division-free form of the same schedule (the
-// p/q recurrence of hines_cell in hx_kernels.cu, with exact reciprocals in
-// place of the device's Newton reciprocal).  Output: rhs holds the solution.
+// p/q recurrence of hines_cell in hx_step.cuh, with exact reciprocals in
+// place of the device's batch-inverted Newton reciprocals).  Output: rhs holds
+// the solution.
 void planned_solve_pq_cpu(const Plan& P, const double* a, const double* b, double* d, double* rhs, bool transposed);
 
 }  // namespace hx

@@ -39,7 +39,7 @@ constexpr int kBlk = 4;
 // tri_block: triangularisation of a chain from node j downwards in projective
 // form.  With d'_k = p_k/q_k and the eliminated rhs r'_k = y_k/q_k:
 //   p_{k-1} = d_{k-1} p_k - A_k U_k q_k,   q_{k-1} = p_k,
-//   y_{k-1} = rhs_{k-1} p_k - A_k y_k,
+//   y_{k-1} = rhs_{k-1} p_k - A_k y_k     (one FMA on the y chain),
 // two FMA chains without division.  For k = j .. j-cnt+1 it stores
 // d[k] = 1/d'_k = q_k/p_k and rhs[k] = r'_k/d'_k = y_k/p_k (the reciprocal is
 // off both chains) and leaves (p, q, y) of node j-cnt.
@@ -59,23 +59,36 @@ __device__ __forceinline__ void tri_block(double* __restrict__ d, double* __rest
     }
 #pragma unroll
     for (int u = 0; u < kBlk; ++u) {
+        pv[u] = 1.0;
         if (!kGuard || u < cnt) {
             pv[u] = pp;
             qv[u] = qq;
             yv[u] = yy;
             const double pn = __fma_rn(dl[u], pp, -(cl[u] * qq));
-            const double yn = __fma_rn(rl[u], pp, -(al[u] * yy));
+            const double yn = __fma_rn(-al[u], yy, rl[u] * pp);
             qq = pp;
             pp = pn;
             yy = yn;
         }
     }
+    // the block's reciprocals 1/p_u from one reciprocal of their product
+    // (batch inversion); the block starts at p in [1, 2) (rescaled by the
+    // caller), so the product of its four pivots' p stays far inside the
+    // double range
+    const double a1 = pv[0] * pv[1], a2 = a1 * pv[2], a3 = a2 * pv[3];
+    double inv = rcp_nz(a3);
+    double ip[kBlk];
+    ip[3] = inv * a2;
+    inv *= pv[3];
+    ip[2] = inv * a1;
+    inv *= pv[2];
+    ip[1] = inv * pv[0];
+    ip[0] = inv * pv[1];
 #pragma unroll
     for (int u = 0; u < kBlk; ++u) {
         if (!kGuard || u < cnt) {
-            const double ip = rcp_nz(pv[u]);
-            d[j - u] = qv[u] * ip;
-            rhs[j - u] = yv[u] * ip;
+            d[j - u] = qv[u] * ip[u];
+            rhs[j - u] = yv[u] * ip[u];
         }
     }
 }
