@@ -6,6 +6,9 @@
 namespace hx {
 
 constexpr int kThreads = 512;  // threads per CTA (one CTA per cell pack, 16 warps, one CTA per SM)
+// split-cell kernels: 8 warps a CTA, so that their larger state fits the
+// registers (232 a thread) without spilling
+constexpr int kSplitThreads = 256;
 
 enum NodeFlag : int { kHasPas = 1, kHasHH = 2 };
 

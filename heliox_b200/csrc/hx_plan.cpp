@@ -148,10 +148,13 @@ std::string split_cell(const std::vector<Branch>& Bin, const std::vector<int>& p
 
 }  // namespace
 
-std::string build_plan(const hx_group_desc& g, int nodes_per_warp, int max_pack_nodes, Plan& P, int nsm) {
+std::string build_plan(const hx_group_desc& g, int nodes_per_warp, int max_pack_nodes, Plan& P, int nsm,
+                       int warps_per_cta) {
+    const int kW = std::max(1, std::min(warps_per_cta, kWarpsPerCta));
     std::string err = validate(g);
     if (!err.empty()) return err;
     P = Plan();
+    P.warps = kW;
     const int n = g.nnode, ncell = g.ncell;
     P.ncell = ncell;
     P.nnode = n;
@@ -236,7 +239,7 @@ std::string build_plan(const hx_group_desc& g, int nodes_per_warp, int max_pack_
     }
     const int nunit = (int)ubr.size();
 
-    // Whole cells are packed into CTAs (at most kWarpsPerCta cells and the
+    // Whole cells are packed into CTAs (at most one cell a warp and the
     // shared-memory capacity in nodes each); the CTA's warps are then shared
     // among its cells in proportion to their nodes (at least one each, largest
     // remainders first), so every thread of a CTA carries about the same
@@ -249,7 +252,7 @@ std::string build_plan(const hx_group_desc& g, int nodes_per_warp, int max_pack_
     const bool balanced = nodes_per_warp <= 0 && nsm > 0 && max_pack_nodes > 0;
     const int npw = nodes_per_warp > 0 ? nodes_per_warp : 144;
     const int maxcell = *std::max_element(usize.begin(), usize.end());
-    int cap = balanced ? max_pack_nodes : npw * kWarpsPerCta;
+    int cap = balanced ? max_pack_nodes : npw * kW;
     if (max_pack_nodes > 0) {
         if (maxcell > max_pack_nodes)
             return "a cell of " + std::to_string(maxcell) + " nodes exceeds the per-CTA capacity of " +
@@ -277,7 +280,7 @@ std::string build_plan(const hx_group_desc& g, int nodes_per_warp, int max_pack_
         const long long per_wave = (long long)avail * (long long)(cap * 0.96);
         int waves = (int)std::max<long long>(1, (total + per_wave - 1) / std::max<long long>(per_wave, 1));
         long long K = (long long)avail * waves;
-        K = std::max<long long>(K, ((long long)order.size() + kWarpsPerCta - 1) / kWarpsPerCta);
+        K = std::max<long long>(K, ((long long)order.size() + kW - 1) / kW);
         K = std::min<long long>(K, (long long)order.size());
         std::set<std::pair<long long, int>> load;  // (nodes, bin)
         for (long long k = 0; k < K; k++) {
@@ -289,7 +292,7 @@ std::string build_plan(const hx_group_desc& g, int nodes_per_warp, int max_pack_
             int b = -1;
             for (auto it = load.begin(); it != load.end(); ++it) {
                 const int k = it->second;
-                if ((int)bins[k].size() < kWarpsPerCta && bin_n[k] + usize[c] <= cap) {
+                if ((int)bins[k].size() < kW && bin_n[k] + usize[c] <= cap) {
                     b = k;
                     load.erase(it);
                     break;
@@ -302,7 +305,7 @@ std::string build_plan(const hx_group_desc& g, int nodes_per_warp, int max_pack_
             }
             bins[b].push_back(c);
             bin_n[b] += usize[c];
-            if ((int)bins[b].size() < kWarpsPerCta) load.insert({bin_n[b], b});
+            if ((int)bins[b].size() < kW) load.insert({bin_n[b], b});
         }
         // drop bins left empty (fewer units than CTAs)
         std::vector<std::vector<int>> kept;
@@ -318,7 +321,7 @@ std::string build_plan(const hx_group_desc& g, int nodes_per_warp, int max_pack_
         for (int c : order) {
             int b = -1;
             for (int k = b0; k < (int)bins.size(); k++)
-                if ((int)bins[k].size() < kWarpsPerCta && bin_n[k] + usize[c] <= cap) {
+                if ((int)bins[k].size() < kW && bin_n[k] + usize[c] <= cap) {
                     b = k;
                     break;
                 }
@@ -360,7 +363,7 @@ std::string build_plan(const hx_group_desc& g, int nodes_per_warp, int max_pack_
     auto assign_warps = [&](const std::vector<int>& cs, std::vector<int>& w) {
         for (int c : cs) w[c] = 1;
         int used = (int)cs.size();
-        while (used < kWarpsPerCta && !cs.empty()) {
+        while (used < kW && !cs.empty()) {
             int best = -1;
             double bt = -1.0;
             for (int c : cs) {
@@ -401,7 +404,7 @@ std::string build_plan(const hx_group_desc& g, int nodes_per_warp, int max_pack_
             na.erase(na.begin() + ia);
             const bool move = (rng() & 1) || bins[o].empty();
             if (move) {
-                if (na.empty() || (int)no.size() >= kWarpsPerCta) continue;
+                if (na.empty() || (int)no.size() >= kW) continue;
                 no.push_back(ca);
             } else {
                 const int io = (int)(rng() % bins[o].size());

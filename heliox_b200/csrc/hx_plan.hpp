@@ -60,6 +60,7 @@ struct Plan {
     // split cell (one cell larger than a CTA): pack 0 holds the top unit, the
     // other packs hold subtree units; links between them are coded in
     // node_parent / node_child / br_parent / br_child as -(2 + subtree id)
+    int warps = kWarpsPerCta;  // warps a CTA of this plan
     int nsub = 0;
     std::vector<int> sub_root;    // GPU node of each subtree root
     std::vector<int> sub_parent;  // GPU node (in pack 0) of its parent
@@ -74,8 +75,10 @@ struct Plan {
 // per warp (0 = default); max_pack_nodes: node capacity of one CTA (shared
 // memory), 0 = unlimited; nsm: SMs of the device (0 = unknown).  With nsm and
 // a capacity but no explicit nodes_per_warp the CTAs are balanced over whole
-// waves of nsm CTAs.  Returns "" on success, else a reason.
-std::string build_plan(const hx_group_desc& g, int nodes_per_warp, int max_pack_nodes, Plan& out, int nsm = 0);
+// waves of nsm CTAs.  warps_per_cta: CTA width the plan is built for (at most
+// that many cells a CTA).  Returns "" on success, else a reason.
+std::string build_plan(const hx_group_desc& g, int nodes_per_warp, int max_pack_nodes, Plan& out, int nsm = 0,
+                       int warps_per_cta = kWarpsPerCta);
 
 // CPU emulation of the kernels' planned Hines solve on GPU-ordered arrays
 // (a, b, d, rhs are GPU-ordered and pack-contiguous).  transposed swaps a/b.

@@ -102,7 +102,7 @@ static void plan_smem(const hx::Plan& P, size_t& fwd, size_t& bwd) {
     Gt.smem_br = P.max_pack_branches;
     Gt.smem_bch = P.max_pack_bch;
     Gt.smem_nch = P.max_pack_nch;
-    Gt.smem_lvl = hx::kWarpsPerCta * (P.max_levels + 1);
+    Gt.smem_lvl = P.warps * (P.max_levels + 1);
     fwd = P.nsub > 0 ? hx::split_fwd_smem_bytes(Gt) : hx::fwd_smem_bytes(Gt);
     bwd = P.nsub > 0 ? hx::split_bwd_smem_bytes(Gt) : hx::bwd_smem_bytes(Gt);
 }
@@ -196,7 +196,11 @@ int hx_plan_check_sm(const hx_group_desc* desc, int nodes_per_warp, int max_pack
                      double* max_abs_diff, double* pq_rel_diff) {
     if (!desc) return -1;
     hx::Plan P;
-    std::string e = hx::build_plan(*desc, nodes_per_warp, max_pack_nodes, P, nsm);
+    // as hx_load_group: a single cell above the capacity is planned for the
+    // split-cell kernels' CTA width
+    const bool split = desc->ncell == 1 && max_pack_nodes > 0 && desc->nnode > max_pack_nodes;
+    std::string e = hx::build_plan(*desc, nodes_per_warp, max_pack_nodes, P, nsm,
+                                   split ? hx::kSplitThreads / 32 : hx::kWarpsPerCta);
     if (!e.empty()) {
         fprintf(stderr, "hx_plan_check: %s\n", e.c_str());
         return -2;
@@ -282,7 +286,8 @@ int hx_load_group(hx_ctx* ctx, const hx_group_desc* desc) {
         cap_nodes = (int)((optin - 4096) / (10 * sizeof(double) + 10));
     }
     cap_nodes = std::min(cap_nodes, 32767);  // 16-bit node tables
-    std::string e = hx::build_plan(*desc, ctx->pack_target, cap_nodes, ctx->P, nsm);
+    const int warps = split_kernels ? hx::kSplitThreads / 32 : hx::kWarpsPerCta;
+    std::string e = hx::build_plan(*desc, ctx->pack_target, cap_nodes, ctx->P, nsm, warps);
     if (!e.empty()) return fail(ctx, "invalid group: " + e);
     for (int shrink = 0; shrink < 8 && desc->nnode > 0; shrink++) {
         // largest synapse count of any pack under this plan
@@ -301,12 +306,12 @@ int hx_load_group(hx_ctx* ctx, const hx_group_desc* desc) {
         Gt.smem_br = Pc.max_pack_branches;
         Gt.smem_bch = Pc.max_pack_bch;
         Gt.smem_nch = Pc.max_pack_nch;
-        Gt.smem_lvl = hx::kWarpsPerCta * (Pc.max_levels + 1);
+        Gt.smem_lvl = Pc.warps * (Pc.max_levels + 1);
         const size_t need = split_kernels ? std::max(hx::split_fwd_smem_bytes(Gt), hx::split_bwd_smem_bytes(Gt))
                                           : std::max(hx::fwd_smem_bytes(Gt, worst), hx::bwd_smem_bytes(Gt, worst));
         if (need <= (size_t)optin) break;
         cap_nodes = (int)(cap_nodes * 0.92);
-        e = hx::build_plan(*desc, ctx->pack_target, cap_nodes, ctx->P, nsm);
+        e = hx::build_plan(*desc, ctx->pack_target, cap_nodes, ctx->P, nsm, warps);
         if (!e.empty()) return fail(ctx, "invalid group: " + e);
     }
     const hx::Plan& P = ctx->P;
@@ -413,7 +418,7 @@ int hx_load_group(hx_ctx* ctx, const hx_group_desc* desc) {
     G.smem_br = P.max_pack_branches;
     G.smem_bch = P.max_pack_bch;
     G.smem_nch = P.max_pack_nch;
-    G.smem_lvl = hx::kWarpsPerCta * (P.max_levels + 1);
+    G.smem_lvl = P.warps * (P.max_levels + 1);
     G.pack_node_off = ctx->pack_node_off.p;
     G.pack_slot_off = ctx->pack_slot_off.p;
     G.pack_br_off = ctx->pack_br_off.p;
@@ -473,8 +478,8 @@ int hx_load_group(hx_ctx* ctx, const hx_group_desc* desc) {
         if (ctx->net) return fail(ctx, "a cell split across CTAs cannot carry network parts");
         HXC(hx::configure_split(sf, sb));
         int per_sm = 0, per_sm_b = 0;
-        HXC(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, hx::split_fwd_kernel_ptr(), hx::kThreads, sf));
-        HXC(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm_b, hx::split_bwd_kernel_ptr(), hx::kThreads, sb));
+        HXC(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, hx::split_fwd_kernel_ptr(), hx::kSplitThreads, sf));
+        HXC(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm_b, hx::split_bwd_kernel_ptr(), hx::kSplitThreads, sb));
         if ((long long)std::min(per_sm, per_sm_b) * nsm < P.npack)
             return fail(ctx, "split cell needs " + std::to_string(P.npack) + " co-resident CTAs (have " +
                                  std::to_string(std::min(per_sm, per_sm_b) * nsm) + ")");

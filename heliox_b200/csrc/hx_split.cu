@@ -170,7 +170,7 @@ __device__ __forceinline__ void back_split(const Meta& M, const Grp& g, const De
 }
 
 // ------------------------------------------------------------------ forward
-__global__ void __launch_bounds__(kThreads, 1) split_fwd_kernel(DevGroup G, DevState S, DevTape T, int write_tape,
+__global__ void __launch_bounds__(kSplitThreads, 1) split_fwd_kernel(DevGroup G, DevState S, DevTape T, int write_tape,
                                                                  DevProbe P, double* __restrict__ trace,
                                                                  const double* __restrict__ tmid, int k0, int k1,
                                                                  DevSplit X) {
@@ -310,7 +310,7 @@ __global__ void __launch_bounds__(kThreads, 1) split_fwd_kernel(DevGroup G, DevS
 }
 
 // ------------------------------------------------------------------ backward
-__global__ void __launch_bounds__(kThreads, 1) split_bwd_kernel(DevGroup G, DevTape T, DevAdj Ad, DevGrad GR,
+__global__ void __launch_bounds__(kSplitThreads, 1) split_bwd_kernel(DevGroup G, DevTape T, DevAdj Ad, DevGrad GR,
                                                                  DevProbe P, const double* __restrict__ dLdv,
                                                                  const double* __restrict__ tmid, int k_hi, int k_lo,
                                                                  DevSplit X) {
@@ -492,7 +492,7 @@ cudaError_t launch_split_fwd(const DevGroup& G, const DevState& S, const DevTape
     DevProbe pr = P;
     DevSplit x = X;
     void* args[] = {&g, &s, &t, &write_tape, &pr, &trace, &tmid, &k0, &k1, &x};
-    return cudaLaunchCooperativeKernel((const void*)split_fwd_kernel, dim3(G.npack), dim3(kThreads), args,
+    return cudaLaunchCooperativeKernel((const void*)split_fwd_kernel, dim3(G.npack), dim3(kSplitThreads), args,
                                        split_fwd_smem_bytes(G), st);
 }
 
@@ -506,7 +506,7 @@ cudaError_t launch_split_bwd(const DevGroup& G, const DevTape& T, const DevAdj& 
     DevProbe pr = P;
     DevSplit x = X;
     void* args[] = {&g, &t, &a, &gr, &pr, &dLdv, &tmid, &k_hi, &k_lo, &x};
-    return cudaLaunchCooperativeKernel((const void*)split_bwd_kernel, dim3(G.npack), dim3(kThreads), args,
+    return cudaLaunchCooperativeKernel((const void*)split_bwd_kernel, dim3(G.npack), dim3(kSplitThreads), args,
                                        split_bwd_smem_bytes(G), st);
 }
 
