@@ -339,12 +339,13 @@ std::string build_plan(const hx_group_desc& g, int nodes_per_warp, int max_pack_
     // latency of its Hines sweeps -- per node of the level-by-level critical
     // path (sum over levels of the longest branch) and per level -- plus the
     // per-node loops, whose time goes with the nodes each thread carries.  The
-    // constants are cycles measured on B200 for the hh + pas kernels; only
-    // their ratios matter.  A CTA finishes with its slowest cell, so warps go
+    // constants are a least-squares fit of per-cell clock64 timings of the
+    // forward + backward kernels on B200 (1024 config-2 cells, one wave; 3 %
+    // mean error); only their ratios matter.  A CTA finishes with its slowest cell, so warps go
     // one at a time to the cell with the largest estimate, and in balanced
     // mode cells are moved / swapped out of the slowest CTA while that lowers
     // its estimate.
-    constexpr double kHinesNode = 260.0, kHinesLevel = 4100.0, kNodeIter = 14200.0;
+    constexpr double kHinesNode = 284.0, kHinesLevel = 3480.0, kNodeIter = 10930.0;
     std::vector<double> uh(nunit, 0.0);
     for (int u = 0; u < nunit; u++) {
         std::map<int, int> longest;
