@@ -85,7 +85,7 @@ struct hx_ctx {
     // plan arrays
     DevBuf<int> pack_node_off, pack_slot_off, pack_br_off, pack_bch_off, pack_nch_off;
     DevBuf<int> cs_node0, cs_nnode, cs_warp0, cs_nwarp, cs_bar, cs_lvl_off, cs_nlev, level_br_off;
-    DevBuf<int> br_head, br_end, br_parent, br_child_off, br_child;
+    DevBuf<int> br_head, br_end, br_parent, br_child_off, br_child, br_child_br;
     DevBuf<int> node_parent, node_child_off, node_child, node_flags, node_ic_off, node_ic;
     // reference instance -> device index, per parameter kind (host + device copies)
     std::vector<int> kmap_h[HX_P_COUNT];

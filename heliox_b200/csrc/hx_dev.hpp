@@ -22,7 +22,7 @@ struct DevGroup {
     const int *pack_node_off, *pack_slot_off, *pack_br_off, *pack_bch_off, *pack_nch_off;
     const int *cs_node0, *cs_nnode, *cs_warp0, *cs_nwarp, *cs_bar, *cs_lvl_off, *cs_nlev;
     const int* level_br_off;
-    const int *br_head, *br_end, *br_parent, *br_child_off, *br_child;
+    const int *br_head, *br_end, *br_parent, *br_child_off, *br_child, *br_child_br;
     const int *node_parent, *node_child_off, *node_child, *node_flags, *node_ic_off, *node_ic;
     const double *a, *b, *cm, *area;
     const double *hh_gnabar, *hh_gkbar, *hh_gl, *hh_el, *hh_ena, *hh_ek;

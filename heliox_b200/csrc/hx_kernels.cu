@@ -67,7 +67,9 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_kernel(DevGroup G, DevState S
     double* sd = srhs + N_;
     double* sa = sd + N_;
     double* sb = sa + N_;
-    double* ssA = sb + N_;                        // kNet: synapse states of the pack
+    double* scd = sb + N_;                        // per-branch contributions of hines_rt
+    double* scr = scd + G.smem_br;
+    double* ssA = scr + G.smem_br;                // kNet: synapse states of the pack
     double* ssB = ssA + (kNet ? N.smem_syn : 0);
     double* send = ssB + (kNet ? N.smem_syn : 0);
     Meta M;
@@ -75,6 +77,7 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_kernel(DevGroup G, DevState S
     if (!setup_pack(G, p, reinterpret_cast<int*>(send), M, g)) return;
     const int pb = G.pack_node_off[p];
     const int i0 = g.nb, i1 = g.nb + g.n;
+    const bool rt = rt_fits(M, g);
     for (int i = i0 + g.tl; i < i1; i += g.nt) {
         sv[i] = S.v[pb + i];
         sa[i] = G.a[pb + i];
@@ -197,7 +200,10 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_kernel(DevGroup G, DevState S
         }
         g.sync();
         // B: Hines solve (rhs := dv)
-        hines_cell<false>(M, g, sa, sb, sd, srhs);
+        if (rt)
+            hines_rt<false>(M, g, sa, sb, sd, srhs, scd, scr);
+        else
+            hines_cell<false>(M, g, sa, sb, sd, srhs);
         // C: v update (the gates follow in the next step's A, or below)
         for (int i = i0 + g.tl; i < i1; i += g.nt) {
             sv[i] = sv[i] + srhs[i];
@@ -269,7 +275,9 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_kernel(DevGroup G, DevTape T,
     double* sd = sw + N_;
     double* sa = sd + N_;
     double* sb = sa + N_;
-    double* slA = sb + N_;  // kNet: synapse adjoints of the pack
+    double* scd = sb + N_;  // per-branch contributions of hines_rt
+    double* scr = scd + G.smem_br;
+    double* slA = scr + G.smem_br;  // kNet: synapse adjoints of the pack
     double* slB = slA + (kNet ? N.smem_syn : 0);
     double* send = slB + (kNet ? N.smem_syn : 0);
     Meta M;
@@ -277,6 +285,7 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_kernel(DevGroup G, DevTape T,
     if (!setup_pack(G, p, reinterpret_cast<int*>(send), M, g)) return;
     const int pb = G.pack_node_off[p];
     const int i0 = g.nb, i1 = g.nb + g.n;
+    const bool rt = rt_fits(M, g);
     const double dt = G.dt, q10 = G.q10;
     double* __restrict__ lv = Ad.lv + pb;
     double* __restrict__ lmv = Ad.lm + pb;
@@ -357,7 +366,10 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_kernel(DevGroup G, DevTape T,
         }
         g.sync();
         // B: w = M^{-T} mu
-        hines_cell<true>(M, g, sa, sb, sd, sw);
+        if (rt)
+            hines_rt<true>(M, g, sa, sb, sd, sw, scd, scr);
+        else
+            hines_cell<true>(M, g, sa, sb, sd, sw);
         // V
         for (int i = i0 + g.tl; i < i1; i += g.nt) {
             const int gi = pb + i;
@@ -595,10 +607,10 @@ cudaError_t launch_f32_to_f64(const float* a, double* b, int n, cudaStream_t st)
 
 // ------------------------------------------------------------------ launchers
 size_t fwd_smem_bytes(const DevGroup& G, int smem_syn) {
-    return sizeof(double) * (5 * (size_t)G.smem_n + 2 * (size_t)smem_syn) + meta_bytes(G);
+    return sizeof(double) * (5 * (size_t)G.smem_n + 2 * (size_t)G.smem_br + 2 * (size_t)smem_syn) + meta_bytes(G);
 }
 size_t bwd_smem_bytes(const DevGroup& G, int smem_syn) {
-    return sizeof(double) * (4 * (size_t)G.smem_n + 2 * (size_t)smem_syn) + meta_bytes(G);
+    return sizeof(double) * (4 * (size_t)G.smem_n + 2 * (size_t)G.smem_br + 2 * (size_t)smem_syn) + meta_bytes(G);
 }
 // split-cell kernels (hx_split.cu) keep the gates / node adjoints in shared memory
 size_t split_fwd_smem_bytes(const DevGroup& G) { return sizeof(double) * 8 * (size_t)G.smem_n + meta_bytes(G); }

@@ -196,7 +196,9 @@ std::string build_plan(const hx_group_desc& g, int nodes_per_warp, int max_pack_
             br.level = pb < 0 ? 0 : B[pb].level + 1;
             int cur = h;
             br.nodes.push_back(cur);
-            while (nchild[cur] == 1) {
+            // an unbranched chain longer than kSegMax is cut into segments
+            // (each a branch whose one child is the next segment)
+            while (nchild[cur] == 1 && (int)br.nodes.size() < kSegMax) {
                 cur = child[child_off[cur]];
                 br.nodes.push_back(cur);
             }
@@ -336,29 +338,39 @@ std::string build_plan(const hx_group_desc& g, int nodes_per_warp, int max_pack_
     }
     // Warps per cell and (balanced mode) the choice of cells per CTA follow an
     // estimate of a cell's forward + backward step time with w warps: the
-    // latency of its Hines sweeps -- per node of the level-by-level critical
-    // path (sum over levels of the longest branch) and per level -- plus the
-    // per-node loops, whose time goes with the nodes each thread carries.  The
-    // constants are a least-squares fit of per-cell clock64 timings of the
-    // forward + backward kernels on B200 (1024 config-2 cells, one wave; 3 %
-    // mean error); only their ratios matter.  A CTA finishes with its slowest cell, so warps go
-    // one at a time to the cell with the largest estimate, and in balanced
-    // mode cells are moved / swapped out of the slowest CTA while that lowers
-    // its estimate.
+    // latency of its Hines solve plus the per-node loops, whose time goes with
+    // the nodes each thread carries.  A cell whose branch segments fit its
+    // threads runs hines_rt, whose latency goes with the longest segment and
+    // the number of segment levels; other cells run hines_cell, whose latency
+    // goes with the level-by-level critical path (sum over levels of the
+    // longest segment) and the levels.  The constants are least-squares fits
+    // of per-cell clock64 timings of the forward + backward kernels on B200
+    // (1024 config-2 cells, one wave; 2-3 % mean error); only their ratios
+    // matter.  A CTA finishes with its slowest cell, so warps go one at a time
+    // to the cell with the largest estimate, and in balanced mode cells are
+    // moved / swapped out of the slowest CTA while that lowers its estimate.
+    constexpr double kRtSeg = 662.0, kRtLevel = 2930.0, kRtIter = 10651.0;
     constexpr double kHinesNode = 284.0, kHinesLevel = 3480.0, kNodeIter = 10930.0;
-    std::vector<double> uh(nunit, 0.0);
+    std::vector<double> uh_old(nunit, 0.0), uh_rt(nunit, 0.0);
+    std::vector<int> useg(nunit, 0);
     for (int u = 0; u < nunit; u++) {
         std::map<int, int> longest;
+        int maxseg = 0;
         for (const Branch& br : ubr[u]) {
             int& l = longest[br.level];
             l = std::max(l, (int)br.nodes.size());
+            maxseg = std::max(maxseg, (int)br.nodes.size());
         }
         double crit = 0.0;
         for (auto& kv : longest) crit += kv.second;
-        uh[u] = kHinesNode * crit + kHinesLevel * (double)longest.size();
+        uh_old[u] = kHinesNode * crit + kHinesLevel * (double)longest.size();
+        uh_rt[u] = kRtSeg * maxseg + kRtLevel * (double)longest.size();
+        useg[u] = (int)ubr[u].size();
     }
     auto unit_time = [&](int u, int w) {
-        return uh[u] + kNodeIter * std::ceil((double)usize[u] / (32.0 * (double)w));
+        const double it = std::ceil((double)usize[u] / (32.0 * (double)w));
+        if (useg[u] <= 32 * w) return uh_rt[u] + kRtIter * it;
+        return uh_old[u] + kNodeIter * it;
     };
     // greedy warps of one CTA; returns the CTA's estimate
     auto assign_warps = [&](const std::vector<int>& cs, std::vector<int>& w) {
@@ -496,18 +508,29 @@ std::string build_plan(const hx_group_desc& g, int nodes_per_warp, int max_pack_
                     gpos++;
                 }
         }
-        // branches of the pack (cell by cell, already level-sorted)
-        for (int c : bins[p])
-            for (const Branch& br : ubr[c]) {
-                P.br_head.push_back(P.ref2gpu[br.head_ref] - base);
-                P.br_end.push_back(P.ref2gpu[br.end_ref] - base);
-                int hp = g.parent[br.head_ref];
-                P.br_parent.push_back(hp < 0 ? -1 : P.ref2gpu[hp] - base);
-                int e = br.end_ref;
-                for (int k = child_off[e + 1] - 1; k >= child_off[e]; k--)
-                    P.br_child.push_back(P.ref2gpu[child[k]] - base);
-                P.br_child_off.push_back((int)P.br_child.size());
+        // branches of the pack (cell by cell, already level-sorted); children
+        // by head node and by pack-local branch id (-1: in another unit)
+        {
+            int pbr = 0;
+            for (int c : bins[p]) {
+                std::unordered_map<int, int> by_head;
+                for (size_t k = 0; k < ubr[c].size(); k++) by_head[ubr[c][k].head_ref] = pbr + (int)k;
+                for (const Branch& br : ubr[c]) {
+                    P.br_head.push_back(P.ref2gpu[br.head_ref] - base);
+                    P.br_end.push_back(P.ref2gpu[br.end_ref] - base);
+                    int hp = g.parent[br.head_ref];
+                    P.br_parent.push_back(hp < 0 ? -1 : P.ref2gpu[hp] - base);
+                    int e = br.end_ref;
+                    for (int k = child_off[e + 1] - 1; k >= child_off[e]; k--) {
+                        P.br_child.push_back(P.ref2gpu[child[k]] - base);
+                        auto it = by_head.find(child[k]);
+                        P.br_child_br.push_back(it == by_head.end() ? -1 : it->second);
+                    }
+                    P.br_child_off.push_back((int)P.br_child.size());
+                }
+                pbr += (int)ubr[c].size();
             }
+        }
         const int pn = gpos - base;
         sum_nodes += pn;
         {
@@ -616,6 +639,7 @@ std::string build_plan(const hx_group_desc& g, int nodes_per_warp, int max_pack_
         P.max_pack_hh = std::max(P.max_pack_hh, hh_cnt);
     }
     if (P.br_child.empty()) P.br_child.push_back(0);
+    if (P.br_child_br.empty()) P.br_child_br.push_back(-1);
     if (P.node_child.empty()) P.node_child.push_back(0);
     if (P.node_ic.empty()) P.node_ic.push_back(0);
     return "";
@@ -736,6 +760,95 @@ void planned_solve_pq_cpu(const Plan& P, const double* a, const double* b, doubl
                 rhs[j] = x;
             }
         });
+}
+
+void planned_solve_rt_cpu(const Plan& P, const double* a, const double* b, double* d, double* rhs, bool transposed) {
+    const double* A = transposed ? b : a;
+    const double* U = transposed ? a : b;
+    std::vector<double> cd(P.br_head.size(), 0.0), cr(P.br_head.size(), 0.0), Fe(P.br_head.size(), 0.0),
+        Ge(P.br_head.size(), 0.0);
+    for (int p = 0; p < P.npack; p++) {
+        const int base = P.pack_node_off[p];
+        const int bbase = P.pack_br_off[p];
+        for (int sl = P.pack_slot_off[p]; sl < P.pack_slot_off[p + 1]; sl++) {
+            const int* lo = &P.level_br_off[P.cs_lvl_off[sl]];
+            const int nlev = P.cs_nlev[sl];
+            auto H = [&](int br) { return base + P.br_head[bbase + br]; };
+            auto E = [&](int br) { return base + P.br_end[bbase + br]; };
+            auto PP = [&](int br) { const int v = P.br_parent[bbase + br]; return v < 0 ? -1 : base + v; };
+            // 1. segment interiors, top-down
+            for (int br = lo[0]; br < lo[nlev]; br++) {
+                const int h = H(br), e = E(br), gb = bbase + br;
+                if (h == e) {
+                    Fe[gb] = A[h];
+                    Ge[gb] = U[h];
+                    cd[gb] = cr[gb] = 0.0;
+                    continue;
+                }
+                double inv = 1.0 / d[h], rp = rhs[h], F = A[h], G = U[h];
+                double dD = F * G * inv, dR = F * rp * inv;
+                d[h] = inv;
+                for (int k = h + 1; k < e; k++) {
+                    const double Dk = std::fma(-(U[k] * A[k]), inv, d[k]);
+                    const double rk = std::fma(-(U[k] * rp), inv, rhs[k]);
+                    F = -(F * A[k]) * inv;
+                    G = -(U[k] * G) * inv;
+                    inv = 1.0 / Dk;
+                    rp = rk;
+                    dD = std::fma(F * G, inv, dD);
+                    dR = std::fma(F * rp, inv, dR);
+                    d[k] = inv;
+                }
+                d[e] = std::fma(-(U[e] * A[e]), inv, d[e]);
+                rhs[e] = std::fma(-(U[e] * rp), inv, rhs[e]);
+                Fe[gb] = -(F * A[e]) * inv;
+                Ge[gb] = -(U[e] * G) * inv;
+                cd[gb] = dD;
+                cr[gb] = dR;
+            }
+            // 2. tree of segment ends
+            for (int L = nlev - 1; L >= 0; L--)
+                for (int br = lo[L]; br < lo[L + 1]; br++) {
+                    const int e = E(br), gb = bbase + br;
+                    double De = d[e], Re = rhs[e];
+                    for (int k = P.br_child_off[gb]; k < P.br_child_off[gb + 1]; k++) {
+                        const int c = bbase + P.br_child_br[k];
+                        De -= cd[c];
+                        Re -= cr[c];
+                    }
+                    const double ie = 1.0 / De, ge = Re * ie, he = Ge[gb] * ie;
+                    cd[gb] = std::fma(Fe[gb], he, cd[gb]);
+                    cr[gb] = std::fma(Fe[gb], ge, cr[gb]);
+                    d[e] = he;
+                    rhs[e] = ge;
+                }
+            for (int L = 0; L < nlev; L++)
+                for (int br = lo[L]; br < lo[L + 1]; br++) {
+                    const int e = E(br), par = PP(br);
+                    double x = rhs[e];
+                    if (par >= 0) x = std::fma(-d[e], rhs[par], x);
+                    rhs[e] = x;
+                }
+            // 3. interiors
+            for (int br = lo[0]; br < lo[nlev]; br++) {
+                const int h = H(br), e = E(br), par = PP(br);
+                if (h == e) continue;
+                double t = rhs[h];
+                if (par >= 0) t = std::fma(-U[h], rhs[par], t);
+                t *= d[h];
+                rhs[h] = t;
+                for (int k = h + 1; k < e; k++) {
+                    t = std::fma(-(U[k] * d[k]), t, rhs[k] * d[k]);
+                    rhs[k] = t;
+                }
+                double x = rhs[e];
+                for (int k = e - 1; k >= h; k--) {
+                    x = std::fma(-(A[k + 1] * d[k]), x, rhs[k]);
+                    rhs[k] = x;
+                }
+            }
+        }
+    }
 }
 
 }  // namespace hx

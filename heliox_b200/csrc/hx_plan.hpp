@@ -25,6 +25,7 @@
 namespace hx {
 
 constexpr int kWarpsPerCta = 16;
+constexpr int kSegMax = 24;  // longest branch segment (longer unbranched chains are cut)
 
 struct Plan {
     int ncell = 0, nnode = 0, nhh = 0, npas = 0, nic = 0;
@@ -46,6 +47,7 @@ struct Plan {
     std::vector<int> br_head, br_end, br_parent;
     std::vector<int> br_child_off;     // size nbranch+1, global offsets into br_child
     std::vector<int> br_child;         // child-head node ids, descending reference index
+    std::vector<int> br_child_br;      // the same children as pack-local branch ids (-1: another unit)
     // nodes in GPU order (global id = pack_node_off[p] + pack-local id)
     std::vector<int> node_parent;      // pack-local, -1 for roots
     std::vector<int> node_child_off;   // size nnode+1, global offsets into node_child
@@ -89,5 +91,10 @@ void planned_solve_cpu(const Plan& P, const double* a, const double* b, double* 
 // place of the device's batch-inverted Newton reciprocals).  Output: rhs holds
 // the solution.
 void planned_solve_pq_cpu(const Plan& P, const double* a, const double* b, double* d, double* rhs, bool transposed);
+
+// CPU emulation of hines_rt (hx_step.cuh): the three-phase reduced-tree solve
+// per cell, exact reciprocals; for plans without a split cell.  Output: rhs
+// holds the solution.
+void planned_solve_rt_cpu(const Plan& P, const double* a, const double* b, double* d, double* rhs, bool transposed);
 
 }  // namespace hx

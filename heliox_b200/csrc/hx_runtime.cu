@@ -244,14 +244,16 @@ int hx_plan_check_sm(const hx_group_desc* desc, int nodes_per_warp, int max_pack
                 dg[gi] = d[ref];
                 rg[gi] = r[ref];
             }
-            std::vector<double> dq = dg, rq = rg;
+            std::vector<double> dq = dg, rq = rg, dt = dg, rt = rg;
             hx::planned_solve_cpu(P, ag.data(), bg.data(), dg.data(), rg.data(), transposed != 0);
             hx::planned_solve_pq_cpu(P, ag.data(), bg.data(), dq.data(), rq.data(), transposed != 0);
+            if (P.nsub == 0) hx::planned_solve_rt_cpu(P, ag.data(), bg.data(), dt.data(), rt.data(), transposed != 0);
             double scale = 0.0;
             for (int gi = 0; gi < n; gi++) scale = std::max(scale, std::fabs(rs[gi]));
             for (int gi = 0; gi < n; gi++) {
                 worst = std::max(worst, std::fabs(rg[gi] - rs[P.gpu2ref[gi]]));
                 worst_pq = std::max(worst_pq, std::fabs(rq[gi] - rs[P.gpu2ref[gi]]) / scale);
+                if (P.nsub == 0) worst_pq = std::max(worst_pq, std::fabs(rt[gi] - rs[P.gpu2ref[gi]]) / scale);
             }
         }
         if (max_abs_diff) *max_abs_diff = worst;
@@ -279,7 +281,7 @@ int hx_load_group(hx_ctx* ctx, const hx_group_desc* desc) {
     HXC(cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, ctx->device));
     const double syn_per_node =
         desc->nnode > 0 ? (double)(std::max(desc->nexpsyn, 0) + std::max(desc->nexp2syn, 0)) / desc->nnode : 0.0;
-    int cap_nodes = (int)((optin - 4096) / (5 * sizeof(double) + 10 + 1.5 * 16 * syn_per_node));
+    int cap_nodes = (int)((optin - 4096) / (5 * sizeof(double) + 12 + 1.5 * 16 * syn_per_node));
     bool split_kernels = false;
     if (desc->ncell == 1 && desc->nnode > cap_nodes) {
         split_kernels = true;
@@ -289,7 +291,7 @@ int hx_load_group(hx_ctx* ctx, const hx_group_desc* desc) {
     const int warps = split_kernels ? hx::kSplitThreads / 32 : hx::kWarpsPerCta;
     std::string e = hx::build_plan(*desc, ctx->pack_target, cap_nodes, ctx->P, nsm, warps);
     if (!e.empty()) return fail(ctx, "invalid group: " + e);
-    for (int shrink = 0; shrink < 8 && desc->nnode > 0; shrink++) {
+    for (int shrink = 0; shrink < 24 && desc->nnode > 0; shrink++) {
         // largest synapse count of any pack under this plan
         const hx::Plan& Pc = ctx->P;
         std::vector<int> nsyn_node(Pc.nnode, 0);
@@ -310,7 +312,7 @@ int hx_load_group(hx_ctx* ctx, const hx_group_desc* desc) {
         const size_t need = split_kernels ? std::max(hx::split_fwd_smem_bytes(Gt), hx::split_bwd_smem_bytes(Gt))
                                           : std::max(hx::fwd_smem_bytes(Gt, worst), hx::bwd_smem_bytes(Gt, worst));
         if (need <= (size_t)optin) break;
-        cap_nodes = (int)(cap_nodes * 0.92);
+        cap_nodes = (int)(cap_nodes * 0.97);
         e = hx::build_plan(*desc, ctx->pack_target, cap_nodes, ctx->P, nsm, warps);
         if (!e.empty()) return fail(ctx, "invalid group: " + e);
     }
@@ -337,6 +339,7 @@ int hx_load_group(hx_ctx* ctx, const hx_group_desc* desc) {
     HXC(ctx->br_parent.upload(P.br_parent, st));
     HXC(ctx->br_child_off.upload(P.br_child_off, st));
     HXC(ctx->br_child.upload(P.br_child, st));
+    HXC(ctx->br_child_br.upload(P.br_child_br, st));
     HXC(ctx->node_parent.upload(P.node_parent, st));
     HXC(ctx->node_child_off.upload(P.node_child_off, st));
     HXC(ctx->node_child.upload(P.node_child, st));
@@ -437,6 +440,7 @@ int hx_load_group(hx_ctx* ctx, const hx_group_desc* desc) {
     G.br_parent = ctx->br_parent.p;
     G.br_child_off = ctx->br_child_off.p;
     G.br_child = ctx->br_child.p;
+    G.br_child_br = ctx->br_child_br.p;
     G.node_parent = ctx->node_parent.p;
     G.node_child_off = ctx->node_child_off.p;
     G.node_child = ctx->node_child.p;

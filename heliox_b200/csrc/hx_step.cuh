@@ -132,6 +132,7 @@ struct Meta {
     int* bp;
     int* bco;   // branch child offsets into bc (size nbr+1)
     int* bc;    // child-branch heads, descending reference index
+    int* bcb;   // the same children as pack-local branch ids (-1: in another CTA)
     int* lvl;   // level tables of the pack's cells (pack-local branch ids)
 };
 
@@ -152,7 +153,7 @@ struct Grp {
 
 // Bytes of the Meta tables in shared memory (a multiple of 16).
 __host__ __device__ inline size_t meta_bytes(const DevGroup& G) {
-    const size_t ints = 4 * (size_t)G.smem_br + 1 + G.smem_bch + G.smem_lvl;
+    const size_t ints = 4 * (size_t)G.smem_br + 1 + 2 * (size_t)G.smem_bch + G.smem_lvl;
     const size_t shorts = 2 * (size_t)G.smem_n + 1 + G.smem_nch;
     const size_t b = 4 * ints + 2 * shorts + (size_t)G.smem_n;
     return (b + 15) & ~(size_t)15;
@@ -167,7 +168,8 @@ __device__ __forceinline__ bool setup_pack(const DevGroup& G, int p, int* ibase,
     M.bp = M.be + G.smem_br;
     M.bco = M.bp + G.smem_br;
     M.bc = M.bco + G.smem_br + 1;
-    M.lvl = M.bc + G.smem_bch;
+    M.bcb = M.bc + G.smem_bch;
+    M.lvl = M.bcb + G.smem_bch;
     M.par = reinterpret_cast<short*>(M.lvl + G.smem_lvl);
     M.cho = M.par + G.smem_n;
     M.ch = M.cho + G.smem_n + 1;
@@ -192,7 +194,10 @@ __device__ __forceinline__ bool setup_pack(const DevGroup& G, int p, int* ibase,
         M.bco[k] = G.br_child_off[br0 + k] - bc0;
     }
     if (tid == 0) M.bco[nbr] = nbc;
-    for (int k = tid; k < nbc; k += nt) M.bc[k] = G.br_child[bc0 + k];
+    for (int k = tid; k < nbc; k += nt) {
+        M.bc[k] = G.br_child[bc0 + k];
+        M.bcb[k] = G.br_child_br[bc0 + k];
+    }
     for (int k = tid; k < l1 - l0; k += nt) M.lvl[k] = G.level_br_off[l0 + k];
     __syncthreads();
     const int w = tid >> 5;
@@ -263,6 +268,124 @@ __device__ __forceinline__ void hines_cell(const Meta& M, const Grp& g, const do
         }
         g.sync();
     }
+}
+
+// hines_rt: the same solve as hines_cell in three phases, for a cell with at
+// most one branch segment per thread (thread tl owns segment lo[0] + tl in
+// every phase, so a segment's fill couplings stay in its registers):
+//  1. every segment eliminates its interior nodes h .. e-1 top-down, keeping
+//     its head's parent P and its end e: d[k] := 1/D'_k on the interior, the
+//     end's diagonal / rhs updated in place, and the fill couplings P-e (Fe in
+//     P's row, Ge in e's row) and the interior's contributions to P's
+//     diagonal / rhs (dD, dR) kept;
+//  2. the tree of segment ends is solved level by level: an end folds in its
+//     child segments' contributions cd, cr (their dD + Fe Ge / D_e, dR +
+//     Fe R_e / D_e), then x_e = R_e/D_e - (Ge/D_e) x_P root-first;
+//  3. every segment solves its interior from x_P and x_e (forward r'' sweep,
+//     then back-substitution).
+// The serial depth is the longest segment (at most kSegMax nodes) twice plus
+// the number of levels, instead of the longest branch of every level.  cd, cr:
+// one double per branch of the pack each.  The elimination order differs from
+// the reference's, so results agree to rounding (the CPU replay of this form
+// is checked against solve_serial by hx_plan_check).
+template <bool kTransposed>
+__device__ __forceinline__ void hines_rt(const Meta& M, const Grp& g, const double* __restrict__ sa,
+                                         const double* __restrict__ sb, double* __restrict__ d,
+                                         double* __restrict__ rhs, double* __restrict__ cd, double* __restrict__ cr) {
+    const double* __restrict__ A = kTransposed ? sb : sa;
+    const double* __restrict__ U = kTransposed ? sa : sb;
+    const int* lo = M.lvl + g.lvl;
+    const int s = lo[0] + g.tl;
+    const bool own = s < lo[g.nlev];
+    int h = 0, e = -1, P = -1, Ls = -1;
+    double Fe = 0.0, Ge = 0.0;
+    if (own) {
+        h = M.bh[s];
+        e = M.be[s];
+        P = M.bp[s];
+        Ls = 0;
+        while (lo[Ls + 1] <= s) ++Ls;
+        if (h == e) {
+            Fe = A[h];
+            Ge = U[h];
+            cd[s] = 0.0;
+            cr[s] = 0.0;
+        } else {
+            double inv = rcp_nz(d[h]);
+            double rp = rhs[h];
+            double F = A[h], G = U[h];
+            double dD = F * G * inv, dR = F * rp * inv;
+            d[h] = inv;
+            for (int k = h + 1; k < e; ++k) {
+                const double Uk = U[k], Ak = A[k];
+                const double Dk = __fma_rn(-(Uk * Ak), inv, d[k]);
+                const double rk = __fma_rn(-(Uk * rp), inv, rhs[k]);
+                F = -(F * Ak) * inv;
+                G = -(Uk * G) * inv;
+                inv = rcp_nz(Dk);
+                rp = rk;
+                dD = __fma_rn(F * G, inv, dD);
+                dR = __fma_rn(F * rp, inv, dR);
+                d[k] = inv;
+            }
+            const double Ue = U[e], Ae = A[e];
+            d[e] = __fma_rn(-(Ue * Ae), inv, d[e]);
+            rhs[e] = __fma_rn(-(Ue * rp), inv, rhs[e]);
+            Fe = -(F * Ae) * inv;
+            Ge = -(Ue * G) * inv;
+            cd[s] = dD;
+            cr[s] = dR;
+        }
+    }
+    g.sync();
+    for (int L = g.nlev - 1; L >= 0; --L) {
+        if (Ls == L) {
+            double De = d[e], Re = rhs[e];
+            const int c1 = M.bco[s + 1];
+            for (int k = M.bco[s]; k < c1; ++k) {
+                const int c = M.bcb[k];
+                De -= cd[c];
+                Re -= cr[c];
+            }
+            const double ie = rcp_nz(De);
+            const double ge = Re * ie, he = Ge * ie;
+            cd[s] = __fma_rn(Fe, he, cd[s]);
+            cr[s] = __fma_rn(Fe, ge, cr[s]);
+            d[e] = he;
+            rhs[e] = ge;
+        }
+        g.sync();
+    }
+    for (int L = 0; L < g.nlev; ++L) {
+        if (Ls == L) {
+            double x = rhs[e];
+            if (P >= 0) x = __fma_rn(-d[e], rhs[P], x);
+            rhs[e] = x;
+        }
+        g.sync();
+    }
+    if (own && h < e) {
+        double t = rhs[h];
+        if (P >= 0) t = __fma_rn(-U[h], rhs[P], t);
+        t *= d[h];
+        rhs[h] = t;
+        for (int k = h + 1; k < e; ++k) {
+            const double ik = d[k];
+            t = __fma_rn(-(U[k] * ik), t, rhs[k] * ik);
+            rhs[k] = t;
+        }
+        double x = rhs[e];
+        for (int k = e - 1; k >= h; --k) {
+            x = __fma_rn(-(A[k + 1] * d[k]), x, rhs[k]);
+            rhs[k] = x;
+        }
+    }
+    g.sync();
+}
+
+// Segments of the group's cell fit its threads (hines_rt applies).
+__device__ __forceinline__ bool rt_fits(const Meta& M, const Grp& g) {
+    return M.lvl[g.lvl + g.nlev] - M.lvl[g.lvl] <= g.nt;
 }
 
 // ------------------------------------------------------------------ per-step I/O

@@ -148,7 +148,7 @@ int hx_get_plan_stats(hx_ctx* ctx, hx_plan_stats* out);
  * diagonally dominant systems, forward and transposed.  *max_abs_diff: largest
  * difference of the schedule replayed in the reference's division form (0 when
  * bit-exact).  *pq_rel_diff: largest difference, relative to max |x|, of the
- * division-free form the kernels use. */
+ * forms the kernels use (projective chains; reduced tree of segments). */
 int hx_plan_check(const hx_group_desc* desc, int nodes_per_warp, hx_plan_stats* out, double* max_abs_diff,
                   double* pq_rel_diff);
 /* The same with a per-CTA node capacity (0 = unlimited): a group of one cell
