@@ -316,7 +316,34 @@ __device__ __forceinline__ void hines_rt(const Meta& M, const Grp& g, const doub
             double F = A[h], G = U[h];
             double dD = F * G * inv, dR = F * rp * inv;
             d[h] = inv;
-            for (int k = h + 1; k < e; ++k) {
+            // interior nodes h+1 .. e-1 in register blocks: operands loaded
+            // ahead of the dependent arithmetic, results stored after it
+            int k = h + 1;
+            for (; k + kBlk <= e; k += kBlk) {
+                double uk[kBlk], ak[kBlk], dk[kBlk], rk[kBlk], iv[kBlk];
+#pragma unroll
+                for (int u = 0; u < kBlk; ++u) {
+                    uk[u] = U[k + u];
+                    ak[u] = A[k + u];
+                    dk[u] = d[k + u];
+                    rk[u] = rhs[k + u];
+                }
+#pragma unroll
+                for (int u = 0; u < kBlk; ++u) {
+                    const double Dk = __fma_rn(-(uk[u] * ak[u]), inv, dk[u]);
+                    const double rn = __fma_rn(-(uk[u] * rp), inv, rk[u]);
+                    F = -(F * ak[u]) * inv;
+                    G = -(uk[u] * G) * inv;
+                    inv = rcp_nz(Dk);
+                    rp = rn;
+                    dD = __fma_rn(F * G, inv, dD);
+                    dR = __fma_rn(F * rp, inv, dR);
+                    iv[u] = inv;
+                }
+#pragma unroll
+                for (int u = 0; u < kBlk; ++u) d[k + u] = iv[u];
+            }
+            for (; k < e; ++k) {
                 const double Uk = U[k], Ak = A[k];
                 const double Dk = __fma_rn(-(Uk * Ak), inv, d[k]);
                 const double rk = __fma_rn(-(Uk * rp), inv, rhs[k]);
@@ -369,13 +396,46 @@ __device__ __forceinline__ void hines_rt(const Meta& M, const Grp& g, const doub
         if (P >= 0) t = __fma_rn(-U[h], rhs[P], t);
         t *= d[h];
         rhs[h] = t;
-        for (int k = h + 1; k < e; ++k) {
+        int k = h + 1;
+        for (; k + kBlk <= e; k += kBlk) {
+            double cu[kBlk], rr[kBlk];
+#pragma unroll
+            for (int u = 0; u < kBlk; ++u) {
+                const double ik = d[k + u];
+                cu[u] = U[k + u] * ik;
+                rr[u] = rhs[k + u] * ik;
+            }
+#pragma unroll
+            for (int u = 0; u < kBlk; ++u) {
+                t = __fma_rn(-cu[u], t, rr[u]);
+                rr[u] = t;
+            }
+#pragma unroll
+            for (int u = 0; u < kBlk; ++u) rhs[k + u] = rr[u];
+        }
+        for (; k < e; ++k) {
             const double ik = d[k];
             t = __fma_rn(-(U[k] * ik), t, rhs[k] * ik);
             rhs[k] = t;
         }
         double x = rhs[e];
-        for (int k = e - 1; k >= h; --k) {
+        k = e - 1;
+        for (; k - kBlk + 1 >= h; k -= kBlk) {
+            double ca[kBlk], rr[kBlk];
+#pragma unroll
+            for (int u = 0; u < kBlk; ++u) {
+                ca[u] = A[k - u + 1] * d[k - u];
+                rr[u] = rhs[k - u];
+            }
+#pragma unroll
+            for (int u = 0; u < kBlk; ++u) {
+                x = __fma_rn(-ca[u], x, rr[u]);
+                rr[u] = x;
+            }
+#pragma unroll
+            for (int u = 0; u < kBlk; ++u) rhs[k - u] = rr[u];
+        }
+        for (; k >= h; --k) {
             x = __fma_rn(-(A[k + 1] * d[k]), x, rhs[k]);
             rhs[k] = x;
         }
