@@ -49,7 +49,7 @@ SEED0 = 20240
 # dram__bytes_write.sum of the captured launch / its compartment-steps; the
 # capture runs the config-2 cells for 100 steps, and the per-step traffic does
 # not depend on the step count).
-BWD_DRAM_BYTES_PER_UNIT = 349.0
+BWD_DRAM_BYTES_PER_UNIT = 322.9
 
 
 def _alg_bytes(g):
