@@ -318,10 +318,6 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_kernel(DevGroup G, DevTape T,
     g.sync();
     for (int k = k_hi - 1; k >= k_lo; --k) {
         const size_t off = (size_t)(k - T.k_base) * (size_t)G.nnode + pb;
-        if (k > k_lo && g.tl < 4) {  // the next step's tape rows of the cell, into L2
-            const double* row = (g.tl == 0 ? T.v : g.tl == 1 ? T.m : g.tl == 2 ? T.h : T.n) + off - G.nnode + i0;
-            prefetch_l2(row, sizeof(double) * (size_t)(i1 - i0));
-        }
         probe_inject(P, q0, q1, dLdv + (size_t)(k + 1) * P.nprobe, lv, g);
         g.sync();
         const double tm = tmid[k];
@@ -370,6 +366,10 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_kernel(DevGroup G, DevTape T,
             hines_rt<true>(M, g, sa, sb, sd, sw, scd, scr);
         else
             hines_cell<true>(M, g, sa, sb, sd, sw);
+        if (k > k_lo && g.tl < 4) {  // the next step's tape rows of the cell, into L2 (read after this phase)
+            const double* row = (g.tl == 0 ? T.v : g.tl == 1 ? T.m : g.tl == 2 ? T.h : T.n) + off - G.nnode + i0;
+            prefetch_l2(row, sizeof(double) * (size_t)(i1 - i0));
+        }
         // V
         for (int i = i0 + g.tl; i < i1; i += g.nt) {
             const int gi = pb + i;

@@ -71,6 +71,53 @@ def test_forward_random_trees(Sim):
     _check_v(tr, ref, g.dt)
 
 
+def _long_chain_and_star():
+    """Two cells that exercise the solver's structural paths: a 1,500-node
+    unbranched chain (cut into 63 segments of at most 24 nodes, solved by the
+    reduced-tree form) and a star of 700 one-node arms (more segments than a
+    CTA has threads: the level-by-level form)."""
+    from heliox_b200.model import CellGroup, MechTable, _f64, _i32, concat_groups
+
+    def cell(parent, seed):
+        n = len(parent)
+        rng = np.random.default_rng(seed)
+        hh_nodes = np.arange(0, n, 7)
+        pas_nodes = np.setdiff1d(np.arange(n), hh_nodes)
+        hh = {k: _f64(np.full(hh_nodes.size, v)) for k, v in synth.HH_STD.items()}
+        return CellGroup(
+            ncell=1,
+            parent=_i32(parent),
+            a=_f64(-rng.uniform(5, 15, n)),
+            b=_f64(-rng.uniform(5, 15, n)),
+            area=_f64(np.full(n, 300.0)),
+            cm=_f64(np.ones(n)),
+            hh=MechTable(_i32(hh_nodes), hh),
+            pas=MechTable(_i32(pas_nodes), {"g": _f64(np.full(pas_nodes.size, 1e-4)),
+                                           "e": _f64(np.full(pas_nodes.size, -65.0))}),
+            iclamp=MechTable(_i32([0]), {"del": _f64([1.0]), "dur": _f64([20.0]), "amp": _f64([0.8])}),
+        )
+
+    chain = cell(np.arange(-1, 1499), 1)
+    star = cell(np.concatenate([[-1], np.zeros(700, dtype=np.int64)]), 2)
+    return concat_groups([chain, star])
+
+
+def test_segmented_chain_and_wide_star(Sim):
+    g = _long_chain_and_star()
+    s = Sim(0)
+    s.load_group(g)
+    probes = np.array([0, 700, 1499, 1500, 1600], dtype=np.int32)
+    T = 1200
+    tr = s.forward_capture(T, probes=probes)
+    ref, _ = O.forward(g, T, probe=probes)
+    _check_v(tr, ref, g.dt)
+    rng = np.random.default_rng(4)
+    dLdv = rng.standard_normal(tr.shape) * 1e-3
+    gg = s.backward(dLdv)
+    _, gr = O.adjoint(g, T, dLdv, probe=probes)
+    _check_g(gg, gr, O.GRAD_KEYS)
+
+
 def test_capture_trace_equals_simulate(Sim):
     g = synth.random_tree_batch(4, seed0=7)
     s = Sim(0)

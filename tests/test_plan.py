@@ -64,6 +64,8 @@ def _star_group(arms=40, arm_len=3):
         (lambda: synth.random_tree_batch(24, seed0=11), 0),
         (lambda: synth.random_tree_batch(24, seed0=11), 4096),
         (lambda: synth.random_tree_cell(3, ncomp=3000, max_levels=40), 0),
+        (lambda: _chain_group(1500), 0),  # 63 segments of <= 24 nodes
+        (lambda: _star_group(arms=700, arm_len=1), 0),  # more segments than a CTA's threads
     ],
 )
 def test_planned_solve_bit_exact(maker, target):
