@@ -128,9 +128,11 @@ const char* hx_last_error(hx_ctx* ctx);
 int hx_abi_version(void);
 /* Launch on this CUDA stream (cudaStream_t passed as void*); NULL = the context's own stream. */
 int hx_set_stream(hx_ctx* ctx, void* stream);
-/* Target cell nodes per warp (0 = default 144): a cell of n nodes is advanced
- * by ceil(n/target) warps (at most 8); cells are packed first-fit into 8-warp
- * CTAs.  Must be called before hx_load_group. */
+/* CTA layout.  0 (default): one 16-warp CTA per SM and as few waves as the
+ * shared memory allows, cells dealt to CTAs by a step-time model and warps
+ * given to the slowest cell of each CTA.  > 0: target cell nodes per warp;
+ * cells are packed first-fit into CTAs of 16 x that many nodes.  Must be
+ * called before hx_load_group. */
 int hx_set_pack_target(hx_ctx* ctx, int nodes_per_warp);
 /* Upper bound on device bytes the forward tape may use; when the full tape
  * does not fit, the backward recomputes checkpointed segments.  0 = default
