@@ -215,3 +215,223 @@ def write_coredat(g: CellGroup, path: str, file_id: int = 0) -> str:
         np.column_stack([np.arange(g.halfgap.n), g.halfgap.ifields["src"]]).astype(np.int32).tofile(
             os.path.join(path, "halfgap.i32"))
     return path
+
+
+# ---------------------------------------------------------------- reader
+class _Reader:
+    def __init__(self, path: str):
+        with open(path, "rb") as f:
+            self.b = f.read()
+        self.pos = 0
+        self.path = path
+
+    def line(self) -> str:
+        end = self.b.index(b"\n", self.pos)
+        s = self.b[self.pos:end].decode()
+        self.pos = end + 1
+        return s
+
+    def int(self) -> int:
+        return int(self.line().split()[0])
+
+    def array(self, chk: List[int], dtype, count: int) -> np.ndarray:
+        tag = self.line()
+        if tag != f"chkpnt {chk[0]}":
+            raise ValueError(f"{self.path}: expected 'chkpnt {chk[0]}', found {tag!r}")
+        chk[0] += 1
+        dt = np.dtype(dtype)
+        a = np.frombuffer(self.b, dtype=dt, count=count, offset=self.pos).copy()
+        self.pos += count * dt.itemsize
+        return a
+
+
+def read_coredat(path: str, file_id=None) -> CellGroup:
+    """Load a CoreNEURON data directory (version 1.8 files) as a ``CellGroup``.
+
+    Reads what ``write_coredat`` writes, in the order the reference's loader
+    reads it (read_filesdat, read_mech, global_vars, read_phase1,
+    read_phase2; src/io/read_coredat.cpp:258-1120): the node arrays, the
+    capacitance, pas, na_ion / k_ion, hh, IClamp, ExpSyn, Exp2Syn, NetStim,
+    HalfGap, gapjunction_lr and neuron_to_neuron_syn_lr instances, the
+    PreSyns and one NetCon per ExpSyn / Exp2Syn instance.  HalfGap sources
+    come from ``halfgap.i32`` when present.  A file with other mechanisms, more
+    than one NetCon on a synapse instance, per-node initial voltages or
+    playback vectors is rejected with a ValueError naming what is not
+    supported.  ``file_id``: the group to read (default: the only one listed in
+    files.dat).
+    """
+    from .model import MechTable, _f64, _i32, empty_table, EXPSYN_FIELDS, EXP2SYN_FIELDS, NETSTIM_FIELDS, \
+        HALFGAP_FIELDS, GAPJ_FIELDS, GRADED_FIELDS
+
+    with open(os.path.join(path, "files.dat")) as f:
+        toks = f.read().split()
+    if toks[0] != VERSION:
+        raise ValueError(f"files.dat version {toks[0]} (supported: {VERSION})")
+    ngroup = int(toks[1])
+    ids = [int(t) for t in toks[2:2 + ngroup]]
+    if file_id is None:
+        if len(ids) != 1:
+            raise ValueError(f"files.dat lists {len(ids)} groups; pass file_id")
+        file_id = ids[0]
+    elif file_id not in ids:
+        raise ValueError(f"group {file_id} not in files.dat")
+    # bbcore_mech.dat: name type pnttype is_art is_ion dsize pdsize ...
+    mech = {}
+    with open(os.path.join(path, "bbcore_mech.dat")) as f:
+        lines = [l for l in f.read().splitlines() if l.strip()]
+    if lines[0].strip() != VERSION:
+        raise ValueError(f"bbcore_mech.dat version {lines[0].strip()} (supported: {VERSION})")
+    k = 2
+    while k < len(lines):
+        t = lines[k].split()
+        name, typ, art, ion, ds, pds = t[0], int(t[1]), int(t[3]), int(t[4]), int(t[5]), int(t[6])
+        mech[typ] = (name, art, ds, pds)
+        k += 2 if ion else 1
+    # globals.dat: "name value" lines up to "0 0", then "secondorder n"
+    glob = {}
+    with open(os.path.join(path, "globals.dat")) as f:
+        glines = f.read().splitlines()
+    for l in glines[1:]:
+        t = l.split()
+        if len(t) == 2 and t[0] == "0" and t[1] == "0":
+            break
+        if len(t) == 2:
+            glob[t[0]] = float(t[1])
+
+    chk = [0]
+    r1 = _Reader(os.path.join(path, f"{file_id}_1.dat"))
+    r1.line()
+    n_presyn, n_netcon = r1.int(), r1.int()
+    output_gid = r1.array(chk, np.int32, n_presyn)
+    netcon_srcgid = r1.array(chk, np.int32, n_netcon)
+
+    r = _Reader(os.path.join(path, f"{file_id}_2.dat"))
+    r.line()
+    ncell, n_outputgid, n_real_output, n = r.int(), r.int(), r.int(), r.int()
+    n_diam, n_mech = r.int(), r.int()
+    mtc = [(r.int(), r.int()) for _ in range(n_mech)]
+    r.int()  # nidata
+    r.int()  # nvdata
+    n_weight = r.int()
+    parent = r.array(chk, np.int32, n)
+    a = r.array(chk, np.float64, n)
+    b = r.array(chk, np.float64, n)
+    area = r.array(chk, np.float64, n)
+    v = r.array(chk, np.float64, n)
+    if n_diam > 0:
+        r.array(chk, np.float64, n)
+    tabs = {}
+    for typ, cnt in mtc:
+        if typ not in mech:
+            raise ValueError(f"mechanism type {typ} is not in bbcore_mech.dat")
+        name, art, ds, pds = mech[typ]
+        if name not in DSIZE:
+            raise ValueError(f"mechanism {name} is not supported by heliox_b200")
+        # artificial cells have no node (the model keeps node 0 as a placeholder)
+        nodes = np.zeros(cnt, dtype=np.int32) if art else r.array(chk, np.int32, cnt)
+        data = r.array(chk, np.float64, cnt * ds).reshape(cnt, ds) if ds else np.zeros((cnt, 0))
+        pdata = None
+        if pds:
+            pdata = r.array(chk, np.int32, cnt * pds).reshape(cnt, pds)
+            if r.int() != 0:
+                raise ValueError(f"{name}: pointer2type entries are not supported")
+            if r.int() != 0:
+                raise ValueError(f"{name}: nmodlrandom entries are not supported")
+        tabs[name] = (nodes, data, pdata)
+    output_vindex = r.array(chk, np.int32, n_outputgid)
+    output_threshold = r.array(chk, np.float64, n_real_output)
+    pnttype = r.array(chk, np.int32, n_netcon)
+    pntindex = r.array(chk, np.int32, n_netcon)
+    weights = r.array(chk, np.float64, n_weight)
+    delay = r.array(chk, np.float64, n_netcon)
+    if r.int() != 0:
+        raise ValueError("BBCOREPOINTER data is not supported")
+    if r.int() != 0:
+        raise ValueError("VecPlayContinuous playback is not supported")
+    if n_weight != n_netcon:
+        raise ValueError("only NetCons with one weight (ExpSyn, Exp2Syn targets) are supported")
+    if n and not np.all(v == v[0]):
+        raise ValueError("per-node initial voltages are not supported (one v_init per group)")
+
+    def tab(name, cols, fields, inames=(), ifill=None):
+        if name not in tabs:
+            return empty_table(fields, inames)
+        nodes, data, pdata = tabs[name]
+        fl = {key: _f64(data[:, c]) for c, key in cols}
+        for key in fields:
+            fl.setdefault(key, _f64(np.zeros(data.shape[0])))
+        ifl = {key: _i32(np.zeros(data.shape[0])) for key in inames}
+        if ifill:
+            ifl.update(ifill(pdata))
+        return MechTable(_i32(nodes), fl, ifl)
+
+    cm = tabs["capacitance"][1][:, 0].copy() if "capacitance" in tabs else np.ones(n)
+    hh = tab("hh", ((0, "gnabar"), (1, "gkbar"), (2, "gl"), (3, "el"), (19, "ena"), (20, "ek")),
+             ("gnabar", "gkbar", "gl", "el", "ena", "ek"))
+    # the ions carry the reversal potentials the hh instances use
+    for ion, key in (("na_ion", "ena"), ("k_ion", "ek")):
+        if ion in tabs and hh.n:
+            inodes, idata, _ = tabs[ion]
+            pos = {int(x): i for i, x in enumerate(inodes)}
+            hh.fields[key] = _f64([idata[pos[int(x)], 0] for x in hh.nodes])
+    pas = tab("pas", ((0, "g"), (1, "e")), ("g", "e"))
+    iclamp = tab("IClamp", ((0, "del"), (1, "dur"), (2, "amp")), ("del", "dur", "amp"))
+    expsyn = tab("ExpSyn", ((0, "tau"), (1, "e")), EXPSYN_FIELDS, ("src",))
+    exp2syn = tab("Exp2Syn", ((0, "tau1"), (1, "tau2"), (2, "e")), EXP2SYN_FIELDS, ("src",))
+    netstim = tab("NetStim", ((0, "interval"), (1, "number"), (2, "start"), (3, "noise")), NETSTIM_FIELDS)
+    halfgap = tab("HalfGap", ((0, "g"),), HALFGAP_FIELDS, ("src",))
+    gapj = tab("gapjunction_lr", ((0, "g"), (1, "w")), GAPJ_FIELDS, ("pre",),
+               lambda pd: {"pre": _i32(pd[:, 2])})
+    graded = tab("neuron_to_neuron_syn_lr", ((0, "w"), (1, "g"), (2, "delta"), (3, "k"), (4, "Vth"), (5, "erev"),
+                                             (6, "dvpre")), GRADED_FIELDS, ("pre",),
+                 lambda pd: {"pre": _i32(pd[:, 2])})
+    # PreSyns: real cells (output_vindex >= 0, the root node) then artificial
+    # cells (-(type + USER_MOD_NUM * index)); NetCon sources map to cell index /
+    # ncell + NetStim index
+    src_of_gid = {}
+    for i in range(n_presyn):
+        ov = int(output_vindex[i])
+        if ov >= 0:
+            if ov >= ncell or parent[ov] >= 0:
+                raise ValueError("a PreSyn not at a cell root is not supported")
+            src_of_gid[int(output_gid[i])] = ov
+        else:
+            typ, idx = (-ov) % USER_MOD_NUM, (-ov) // USER_MOD_NUM
+            if mech.get(typ, ("",))[0] != "NetStim":
+                raise ValueError("artificial-cell PreSyns other than NetStim are not supported")
+            src_of_gid[int(output_gid[i])] = ncell + idx
+    ps_thresh = np.full(ncell, 10.0)
+    for i in range(min(n_real_output, n_presyn)):
+        ov = int(output_vindex[i])
+        if 0 <= ov < ncell:
+            ps_thresh[ov] = output_threshold[i]
+    seen = {TYPE["ExpSyn"]: np.zeros(expsyn.n, bool), TYPE["Exp2Syn"]: np.zeros(exp2syn.n, bool)}
+    for j in range(n_netcon):
+        t, idx = int(pnttype[j]), int(pntindex[j])
+        name = mech.get(t, ("",))[0]
+        if name not in ("ExpSyn", "Exp2Syn"):
+            raise ValueError(f"NetCon target {name or t} is not supported")
+        tb = expsyn if name == "ExpSyn" else exp2syn
+        if seen[TYPE[name]][idx]:
+            raise ValueError(f"more than one NetCon on {name} instance {idx} is not supported")
+        seen[TYPE[name]][idx] = True
+        g_src = int(netcon_srcgid[j])
+        if g_src not in src_of_gid:
+            raise ValueError(f"NetCon source gid {g_src} has no PreSyn in this group")
+        tb.ifields["src"][idx] = src_of_gid[g_src]
+        tb.fields["weight"][idx] = weights[j]
+        tb.fields["delay"][idx] = delay[j]
+    for name, s in seen.items():
+        if not s.all():
+            raise ValueError("a synapse instance without a NetCon is not supported")
+    hg_path = os.path.join(path, "halfgap.i32")
+    if halfgap.n and os.path.exists(hg_path):
+        pairs = np.fromfile(hg_path, dtype=np.int32).reshape(-1, 2)
+        halfgap.ifields["src"][pairs[:, 0]] = pairs[:, 1]
+    g = CellGroup(ncell=int(ncell), parent=_i32(parent), a=_f64(a), b=_f64(b), area=_f64(area), cm=_f64(cm),
+                  hh=hh, pas=pas, iclamp=iclamp, celsius=glob.get("celsius", 6.3), dt=glob.get("dt", 0.025),
+                  v_init=float(v[0]) if n else -65.0, name=os.path.basename(os.path.normpath(path)),
+                  expsyn=expsyn, exp2syn=exp2syn, netstim=netstim, halfgap=halfgap, gapjunction=gapj,
+                  graded=graded, ps_thresh=_f64(ps_thresh))
+    g.validate()
+    return g
