@@ -118,6 +118,8 @@ SIGNATURES = {
     "hx_get_plan_stats": (C.c_int, [C.c_void_p, C.POINTER(PlanStats)]),
     "hx_plan_check": (C.c_int, [C.POINTER(GroupDesc), C.c_int, C.POINTER(PlanStats), _dp, _dp]),
     "hx_plan_check_cap": (C.c_int, [C.POINTER(GroupDesc), C.c_int, C.c_int, C.POINTER(PlanStats), _dp, _dp]),
+    "hx_simulate_and_adjoint_into": (C.c_int, [C.c_void_p, _fp, C.c_int, C.c_int, _ip, C.c_int, _fp, _fp, C.c_int,
+                                               _ip, _ip, _ip, _fp, C.c_double, C.c_double, C.c_double, C.c_int]),
     "hx_plan_check_sm": (C.c_int, [C.POINTER(GroupDesc), C.c_int, C.c_int, C.c_int, C.POINTER(PlanStats), _dp, _dp]),
     "hx_set_param": (C.c_int, [C.c_void_p, C.c_int, _dp, C.c_int]),
     "hx_get_param": (C.c_int, [C.c_void_p, C.c_int, _dp, C.c_int]),

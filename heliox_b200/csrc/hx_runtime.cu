@@ -898,6 +898,36 @@ int hx_reduce_grads_f32(hx_ctx* ctx, int n, const int* kind, const int* index, c
     return 0;
 }
 
+int hx_simulate_and_adjoint_into(hx_ctx* ctx, const float* dLtdv, int nstep, int n_output, const int32_t* poutput,
+                                 int N, float* dw_out_n, float* dx, int n_param, const int* kind, const int* index,
+                                 const int32_t* dest, const float* scale, double v_init, double grad_scale,
+                                 double grad_l2norm_threshold, int clip_strategy) {
+    if (!ctx || nstep < 0 || n_output < 0 || N < 0 || n_param < 0 || (n_output && (!dLtdv || !poutput)) ||
+        (N && !dw_out_n))
+        return fail(ctx, "bad argument");
+    if (dx) return fail(ctx, "input gradients (dx) are not produced by the exact adjoint entry; pass NULL");
+    if (clip_strategy != 0 && !(grad_l2norm_threshold > 0.0)) return fail(ctx, "invalid grad_l2norm_threshold");
+    std::vector<int> probes(poutput, poutput + n_output);
+    if (hx_forward_capture(ctx, nstep, v_init, n_output, probes.data(), nullptr)) return -1;
+    // dL/d(trace): row 0 (the initial state) carries no loss; row t+1 of the
+    // trace is row t of dLtdv
+    std::vector<double> dl((size_t)(nstep + 1) * (size_t)n_output, 0.0);
+    for (size_t e = 0; e < (size_t)nstep * (size_t)n_output; e++) dl[(size_t)n_output + e] = (double)dLtdv[e];
+    if (hx_backward(ctx, dl.data(), nullptr)) return -1;
+    if (hx_reduce_grads_f32(ctx, n_param, kind, index, dest, scale, dw_out_n, N)) return -1;
+    double ss = 0.0;
+    for (int c = 0; c < N; c++) {
+        dw_out_n[c] = (float)((double)dw_out_n[c] * grad_scale);
+        ss += (double)dw_out_n[c] * (double)dw_out_n[c];
+    }
+    const double l2 = std::sqrt(ss);
+    if (clip_strategy != 0 && std::isfinite(l2) && l2 > grad_l2norm_threshold) {
+        const double f = grad_l2norm_threshold / l2;
+        for (int c = 0; c < N; c++) dw_out_n[c] = (float)((double)dw_out_n[c] * f);
+    }
+    return 0;
+}
+
 int hx_mse_loss_grad_dev(hx_ctx* ctx, const double* trace_dev, const double* target_dev, int nrow, int ncol,
                          double* dLdv_dev, double* loss_dev) {
     if (!ctx || !trace_dev || !target_dev || !dLdv_dev || !loss_dev || nrow < 1 || ncol < 0)

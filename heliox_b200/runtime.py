@@ -284,6 +284,35 @@ class Sim:
                                         _lib.fptr(scale), _lib.fptr(out), int(n_out)), "hx_reduce_grads_f32")
         return out
 
+    def simulate_and_adjoint_into(self, dLtdv: np.ndarray, probes, handles: Sequence[int], dest: np.ndarray,
+                                  scale: np.ndarray, n_out: int, v_init: Optional[float] = None,
+                                  grad_scale: float = 1.0, grad_l2norm_threshold: float = 0.0,
+                                  clip_strategy: int = 0) -> np.ndarray:
+        """One call in the shape of the reference's simulate_and_replay_dw_dx_streaming_into:
+        forward (probes recorded), exact adjoint of dL/d(probe trace) = dLtdv
+        (float32, nstep x nprobe; row t is step t+1), column reduction
+        out[dest[j]] += scale[j] * grad[handle j] times grad_scale, optional
+        L2-norm clipping of the result.  Returns out (float32[n_out])."""
+        p = self._probe_arr(probes)
+        d = np.ascontiguousarray(dLtdv, dtype=np.float32)
+        if d.ndim != 2 or d.shape[1] != p.shape[0]:
+            raise ValueError("dLtdv must have shape (nstep, nprobe)")
+        hk = np.array([split_handle(h)[0] for h in handles], dtype=np.int32)
+        hi = np.array([split_handle(h)[1] for h in handles], dtype=np.int32)
+        dest = np.ascontiguousarray(dest, dtype=np.int32)
+        scale = np.ascontiguousarray(scale, dtype=np.float32)
+        out = np.zeros(int(n_out), dtype=np.float32)
+        vi = self.group.v_init if v_init is None else v_init
+        self._check(
+            self._L.hx_simulate_and_adjoint_into(self._ctx, _lib.fptr(d), int(d.shape[0]), int(p.shape[0]),
+                                                 _lib.iptr(p), int(n_out), _lib.fptr(out), None,
+                                                 int(hk.shape[0]), _lib.iptr(hk), _lib.iptr(hi), _lib.iptr(dest),
+                                                 _lib.fptr(scale), float(vi), float(grad_scale),
+                                                 float(grad_l2norm_threshold), int(clip_strategy)),
+            "hx_simulate_and_adjoint_into")
+        self._nstep, self._probes = int(d.shape[0]), p
+        return out
+
     # ------------------------------------------------------------------ device-pointer variants
     def forward_capture_dev(self, nstep: int, trace_ptr: int, v_init: Optional[float] = None, probes=None):
         """Forward + tape with the probe trace written to a device buffer ((nstep+1) x nprobe doubles)."""

@@ -231,6 +231,24 @@ int hx_backward_dev(hx_ctx* ctx, const double* dLdv_dev, double* const* grads_de
 int hx_reduce_grads_f32(hx_ctx* ctx, int n, const int* kind, const int* index, const int32_t* dest,
                         const float* scale, float* out, int n_out);
 
+/* One-call exact-adjoint counterpart of LearnRuntime::
+ * simulate_and_replay_dw_dx_streaming_into (src/runtime_api/learn/
+ * LearnRuntime.h:72-100): a forward of nstep steps from v_init recording the
+ * n_output probe nodes poutput, the exact adjoint of dL/d(probe trace) given
+ * by dLtdv (float32, nstep x n_output; row t is step t+1, the initial state
+ * carries no loss), then dw_out_n[dest[j]] += scale[j] * dL/d(param j) for the
+ * n_param handles (kind, index) -- the reference's pure_i / didv / didvpre
+ * handle lists passed as one list -- times grad_scale (dw_out_n, N floats,
+ * zeroed first).  With clip_strategy != 0, dw_out_n is scaled down to L2 norm
+ * grad_l2norm_threshold when above it (the exact adjoint needs no clipping
+ * inside the sweep; the reference clips its LRDS sensitivities there).  The
+ * LRDS-only knobs (k_mul, percise, eps, clip_check_every) have no counterpart;
+ * input gradients are not produced: dx must be NULL. */
+int hx_simulate_and_adjoint_into(hx_ctx* ctx, const float* dLtdv, int nstep, int n_output, const int32_t* poutput,
+                                 int N, float* dw_out_n, float* dx, int n_param, const int* kind, const int* index,
+                                 const int32_t* dest, const float* scale, double v_init, double grad_scale,
+                                 double grad_l2norm_threshold, int clip_strategy);
+
 /* ---- optimizer ---------------------------------------------------------------------- */
 /* Adam over parameter instances, updating the device parameters in place.
  * Mirrors Simulate::create_optimizer / configure_optimizer /

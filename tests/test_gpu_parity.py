@@ -241,3 +241,44 @@ def test_reduce_grads_columns(Sim):
     for j in range(n):
         ref[dest[j]] += float(scale[j]) * gg["hh.gnabar"][idx[j]]
     np.testing.assert_allclose(out, ref.astype(np.float32), rtol=1e-6, atol=1e-30)
+
+
+def test_simulate_and_adjoint_into(Sim):
+    """The one-call entry (shape of LearnRuntime::simulate_and_replay_dw_dx_streaming_into)
+    equals forward_capture + backward + the column reduction, scaled and clipped."""
+    g = synth.random_tree_batch(3, seed0=9)
+    T = 300
+    probes = g.soma_nodes().astype(np.int32)
+    rng = np.random.default_rng(6)
+    dLtdv = (rng.standard_normal((T, probes.shape[0])) * 1e-2).astype(np.float32)
+    n = 40
+    idx = rng.integers(0, g.hh.n, n)
+    dest = rng.integers(0, 5, n).astype(np.int32)
+    scale = rng.uniform(0.5, 2, n).astype(np.float32)
+
+    s = Sim(0)
+    s.load_group(g)
+    handles = [s.get_variable_handle("hh", "gkbar", int(i)) for i in idx]
+    tr = s.forward_capture(T, probes=probes)
+    dl = np.zeros_like(tr)
+    dl[1:] = dLtdv
+    gg = s.backward(dl, keys=("hh.gkbar",))
+    ref = np.zeros(5)
+    for j in range(n):
+        ref[dest[j]] += float(scale[j]) * gg["hh.gkbar"][idx[j]]
+
+    out = s.simulate_and_adjoint_into(dLtdv, probes, handles, dest, scale, 5, grad_scale=0.5)
+    np.testing.assert_allclose(out, (0.5 * ref).astype(np.float32), rtol=1e-6, atol=1e-30)
+    norm = float(np.linalg.norm(0.5 * ref))
+    clipped = s.simulate_and_adjoint_into(dLtdv, probes, handles, dest, scale, 5, grad_scale=0.5,
+                                          grad_l2norm_threshold=0.25 * norm, clip_strategy=1)
+    np.testing.assert_allclose(np.linalg.norm(clipped.astype(np.float64)), 0.25 * norm, rtol=1e-5)
+    np.testing.assert_allclose(clipped / np.linalg.norm(clipped), out / np.linalg.norm(out), rtol=1e-5, atol=1e-7)
+    # input gradients are not produced: a dx buffer is an error
+    from heliox_b200 import _lib
+
+    dx = np.zeros(4, dtype=np.float32)
+    rc = s._L.hx_simulate_and_adjoint_into(s._ctx, _lib.fptr(dLtdv), T, probes.shape[0], _lib.iptr(probes), 5,
+                                           _lib.fptr(out), _lib.fptr(dx), 0, None, None, None, None,
+                                           float(g.v_init), 1.0, 0.0, 0)
+    assert rc != 0
