@@ -55,12 +55,41 @@ MECH_TABLE: List[Tuple[int, str, int, int, int, int, int, float]] = [
     (13, "gapjunction_lr", 6, 0, 0, 7, 3, 0.0),
     (14, "neuron_to_neuron_syn_lr", 7, 0, 0, 19, 3, 0.0),
 ]
+# library mechanisms (written only for groups that carry them): ca_ion and the
+# user-mech channel set; dsize covers the columns var_in_coredata_idx reads
+# (CaDynamics_E2.cu:57-66, CA_HVA.cu, Ca_LVAst.cu, Im.cu, K_Pst.cu, K_Tst.cu,
+# NaTg.cu:62-70, Nap_Et2.cu, SK_E2.cu:58-62, SKv3_1.cu)
+LIB_MECH_TABLE: List[Tuple[int, str, int, int, int, int, int, float]] = [
+    (15, "ca_ion", 0, 0, 1, 5, 1, 2.0),
+    (16, "CaDynamics_E2", 0, 0, 0, 6, 0, 0.0),
+    (17, "Ca_HVA", 0, 0, 0, 15, 0, 0.0),
+    (18, "Ca_LVAst", 0, 0, 0, 10, 0, 0.0),
+    (19, "Im", 0, 0, 0, 9, 0, 0.0),
+    (20, "K_Pst", 0, 0, 0, 10, 0, 0.0),
+    (21, "K_Tst", 0, 0, 0, 10, 0, 0.0),
+    (22, "NaTg", 0, 0, 0, 9, 0, 0.0),
+    (23, "Nap_Et2", 0, 0, 0, 5, 0, 0.0),
+    (24, "SK_E2", 0, 0, 0, 4, 0, 0.0),
+    (25, "SKv3_1", 0, 0, 0, 4, 0, 0.0),
+]
+# data column of each library field (its var_in_coredata_idx); SK_E2.zTau is
+# the GLOBAL zTau_SK_E2 of globals.dat (SK_E2.cu:65-66)
+LIB_COLUMNS = {
+    "CaDynamics_E2": {"gamma": 0, "decay": 1, "depth": 2, "minCai": 3},
+    "Ca_HVA": {"gbar": 0}, "Ca_LVAst": {"gCa_LVAstbar": 0}, "Im": {"gImbar": 0}, "K_Pst": {"gK_Pstbar": 0},
+    "K_Tst": {"gK_Tstbar": 0},
+    "NaTg": {"gNaTgbar": 0, "vshifth": 1, "vshiftm": 2, "slopeh": 3, "slopem": 4},
+    "Nap_Et2": {"gNap_Et2bar": 0}, "SK_E2": {"gSK_E2bar": 0}, "SKv3_1": {"gSKv3_1bar": 0},
+}
+# ca_ion iontype with Nernst reversal potentials at finitialize and every step
+# (eion.cuh:165, 181: bits 040 and 0100)
+IONTYPE_NERNST = 0o140
 # a NetStim's PreSyn is written as output_vindex -(type + USER_MOD_NUM * index)
 # (read_coredat.cpp:930-940 with the loader's default user_mod_num 1000)
 USER_MOD_NUM = 1000
-TYPE = {m[1]: m[0] for m in MECH_TABLE}
-DSIZE = {m[1]: m[5] for m in MECH_TABLE}
-PDSIZE = {m[1]: m[6] for m in MECH_TABLE}
+TYPE = {m[1]: m[0] for m in MECH_TABLE + LIB_MECH_TABLE}
+DSIZE = {m[1]: m[5] for m in MECH_TABLE + LIB_MECH_TABLE}
+PDSIZE = {m[1]: m[6] for m in MECH_TABLE + LIB_MECH_TABLE}
 
 
 
@@ -89,9 +118,10 @@ def write_coredat(g: CellGroup, path: str, file_id: int = 0) -> str:
     with open(os.path.join(path, "files.dat"), "w") as f:
         f.write(f"{VERSION}\n1\n{file_id}\n")
     # bbcore_mech.dat: types 2.. in order (types 0 and 1 are unused)
+    table = MECH_TABLE + (LIB_MECH_TABLE if g.lib else [])
     with open(os.path.join(path, "bbcore_mech.dat"), "w") as f:
-        f.write(f"{VERSION}\n{MECH_TABLE[-1][0] + 1}\n")
-        for (t, name, pnt, art, ion, ds, pds, charge) in MECH_TABLE:
+        f.write(f"{VERSION}\n{table[-1][0] + 1}\n")
+        for (t, name, pnt, art, ion, ds, pds, charge) in table:
             f.write(f"{name} {t} {pnt} {art} {ion} {ds} {pds} 0\n")
             if ion:
                 f.write(f"{charge}\n")
@@ -100,6 +130,9 @@ def write_coredat(g: CellGroup, path: str, file_id: int = 0) -> str:
         f.write(f"{VERSION}\n")
         f.write(f"celsius {g.celsius:.17g}\n")
         f.write(f"dt {g.dt:.17g}\n")
+        sk = g.lib.get("SK_E2")
+        if sk is not None and sk.n:
+            f.write(f"zTau_SK_E2 {float(sk.fields['zTau'][0]):.17g}\n")
         f.write("0 0\n")
         f.write("secondorder 0\n")
 
@@ -132,11 +165,18 @@ def write_coredat(g: CellGroup, path: str, file_id: int = 0) -> str:
         d[:, 0] = pas.fields["g"]
         d[:, 1] = pas.fields["e"]
         mechs.append(("pas", pas.nodes, d, None))
+    for ion, key in (("na_ion", "ena"), ("k_ion", "ek")):
+        # instances on the hh nodes and the library's ion nodes (equal erev where both)
+        lt = g.lib.get(ion)
+        nodes = np.union1d(hh.nodes, lt.nodes if lt is not None else np.zeros(0, np.int32)).astype(np.int32)
+        if not nodes.size:
+            continue
+        d = np.zeros((nodes.size, DSIZE[ion]))
+        d[np.searchsorted(nodes, hh.nodes), 0] = hh.fields[key]
+        if lt is not None and lt.n:
+            d[np.searchsorted(nodes, lt.nodes), 0] = lt.fields[key]
+        mechs.append((ion, nodes, d, np.zeros((nodes.size, 1), dtype=np.int32)))
     if hh.n:
-        for ion, key in (("na_ion", "ena"), ("k_ion", "ek")):
-            d = np.zeros((hh.n, DSIZE[ion]))
-            d[:, 0] = hh.fields[key]
-            mechs.append((ion, hh.nodes, d, np.zeros((hh.n, 1), dtype=np.int32)))
         d = np.zeros((hh.n, DSIZE["hh"]))
         d[:, 0] = hh.fields["gnabar"]
         d[:, 1] = hh.fields["gkbar"]
@@ -171,6 +211,20 @@ def write_coredat(g: CellGroup, path: str, file_id: int = 0) -> str:
     point("neuron_to_neuron_syn_lr", g.graded, ((0, "w"), (1, "g"), (2, "delta"), (3, "k"), (4, "Vth"), (5, "erev"),
                                                 (6, "dvpre")), pointer=g.graded.ifields["pre"])
     npnt = npnt[0]
+    ca = g.lib.get("ca_ion")
+    if ca is not None and ca.n:
+        d = np.zeros((ca.n, DSIZE["ca_ion"]))
+        d[:, 0], d[:, 1], d[:, 2] = ca.fields["eca"], ca.fields["cai"], ca.fields["cao"]
+        it = np.where(ca.ifields["nernst"] != 0, IONTYPE_NERNST, 0).astype(np.int32).reshape(-1, 1)
+        mechs.append(("ca_ion", ca.nodes, d, it))
+    for name, cols in LIB_COLUMNS.items():
+        tab = g.lib.get(name)
+        if tab is None or not tab.n:
+            continue
+        d = np.zeros((tab.n, DSIZE[name]))
+        for key, c in cols.items():
+            d[:, c] = tab.fields[key]
+        mechs.append((name, tab.nodes, d, None))
     counts = {name: (g.netstim.n if name == "NetStim" else int(nodes.shape[0])) for name, nodes, _, _ in mechs}
 
     # <id>_2.dat

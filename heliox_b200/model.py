@@ -62,6 +62,36 @@ GAPJ_FIELDS = ("g", "w")
 GRADED_FIELDS = ("w", "g", "delta", "k", "Vth", "erev", "dvpre")
 SPIKE_THRESHOLD = 10.0
 
+# Library mechanisms: the ions and the user-mech channel set (name, fields,
+# number of leading trainable fields), in CoreNEURON type order.  Field names
+# are the reference's RANGE names (src/mech/user-mech/<name>.cu
+# var_in_coredata_idx); ion fields follow eion.cuh:81-86 (cai is the initial
+# concentration, ifields['nernst'] = 1 recomputes eca from cai/cao every step,
+# eion.cuh:155-166).  na_ion / k_ion on an hh node must carry hh's ena / ek.
+LIB_MECHS = (
+    ("na_ion", ("ena",), 0),
+    ("k_ion", ("ek",), 0),
+    ("ca_ion", ("cai", "cao", "eca"), 0),
+    ("CaDynamics_E2", ("gamma", "decay", "depth", "minCai"), 4),
+    ("Ca_HVA", ("gbar",), 1),
+    ("Ca_LVAst", ("gCa_LVAstbar",), 1),
+    ("Im", ("gImbar",), 1),
+    ("K_Pst", ("gK_Pstbar",), 1),
+    ("K_Tst", ("gK_Tstbar",), 1),
+    ("NaTg", ("gNaTgbar", "vshifth", "vshiftm", "slopeh", "slopem"), 1),
+    ("Nap_Et2", ("gNap_Et2bar",), 1),
+    ("SK_E2", ("gSK_E2bar", "zTau"), 1),
+    ("SKv3_1", ("gSKv3_1bar",), 1),
+)
+LIB_NAMES = tuple(m[0] for m in LIB_MECHS)
+LIB_FIELDS = {m[0]: m[1] for m in LIB_MECHS}
+LIB_NTRAIN = {m[0]: m[2] for m in LIB_MECHS}
+# which ion each library mechanism reads (erev / concentration) or writes
+LIB_IONS = {
+    "CaDynamics_E2": ("ca",), "Ca_HVA": ("ca",), "Ca_LVAst": ("ca",), "Im": ("k",), "K_Pst": ("k",),
+    "K_Tst": ("k",), "NaTg": ("na",), "Nap_Et2": ("na",), "SK_E2": ("k", "ca"), "SKv3_1": ("k",),
+}
+
 
 def _f64(x) -> np.ndarray:
     return np.ascontiguousarray(np.asarray(x, dtype=F64))
@@ -118,6 +148,7 @@ class CellGroup:
     graded: Optional[MechTable] = None
     ps_thresh: Optional[np.ndarray] = None
     netstim_rng: int = 0
+    lib: Dict[str, MechTable] = field(default_factory=dict)
 
     def __post_init__(self):
         if self.expsyn is None:
@@ -223,6 +254,45 @@ class CellGroup:
             raise ValueError("ExpSyn.tau must be positive")
         if self.ps_thresh.shape != (self.ncell,) or self.ps_thresh.dtype != F64:
             raise ValueError(f"ps_thresh must be float64[{self.ncell}]")
+        self._validate_lib()
+
+    def _validate_lib(self) -> None:
+        n = self.nnode
+        for nm, tab in self.lib.items():
+            if nm not in LIB_FIELDS:
+                raise ValueError(f"unknown library mechanism {nm!r}")
+            if tab.n and (np.any(tab.nodes < 0) or np.any(tab.nodes >= n)):
+                raise ValueError(f"{nm} node index out of range")
+            if tab.n > 1 and np.any(np.diff(tab.nodes) <= 0):
+                raise ValueError(f"{nm} nodes must be sorted, one instance per node")
+            for k in LIB_FIELDS[nm]:
+                v = tab.fields.get(k)
+                if v is None or v.shape != (tab.n,) or v.dtype != F64:
+                    raise ValueError(f"{nm}.{k} must be float64[{tab.n}]")
+        if "ca_ion" in self.lib:
+            nz = self.lib["ca_ion"].ifields.get("nernst")
+            if nz is None or nz.shape != (self.lib["ca_ion"].n,) or nz.dtype != I32:
+                raise ValueError("ca_ion.nernst must be int32[n]")
+            if np.any(self.lib["ca_ion"].fields["cai"] <= 0):
+                raise ValueError("ca_ion.cai must be positive")
+        for nm, ions in LIB_IONS.items():
+            tab = self.lib.get(nm)
+            if tab is None or not tab.n:
+                continue
+            for ion in ions:
+                it = self.lib.get(ion + "_ion")
+                if it is None or not np.all(np.isin(tab.nodes, it.nodes)):
+                    raise ValueError(f"{nm} needs {ion}_ion on each of its nodes")
+        for ion, key in (("na_ion", "ena"), ("k_ion", "ek")):
+            it = self.lib.get(ion)
+            if it is None or not it.n or not self.hh.n:
+                continue
+            common, ia, ib = np.intersect1d(it.nodes, self.hh.nodes, return_indices=True)
+            if common.size and not np.array_equal(it.fields[key][ia], self.hh.fields[key][ib]):
+                raise ValueError(f"{ion}.{key} differs from hh.{key} on a shared node")
+        sk = self.lib.get("SK_E2")
+        if sk is not None and sk.n and np.any(sk.fields["zTau"] != sk.fields["zTau"][0]):
+            raise ValueError("SK_E2.zTau is a GLOBAL of the mechanism: one value for all instances")
 
     def copy(self) -> "CellGroup":
         return CellGroup(
@@ -248,6 +318,7 @@ class CellGroup:
             graded=self.graded.copy(),
             ps_thresh=self.ps_thresh.copy(),
             netstim_rng=self.netstim_rng,
+            lib={k: v.copy() for k, v in self.lib.items()},
         )
 
     # ------------------------------------------------------------ parameters
@@ -259,11 +330,35 @@ class CellGroup:
         if tab is None:
             if mech == "capacitance" and var == "cm":
                 return self.cm
+            if mech in self.lib and var in self.lib[mech].fields:
+                return self.lib[mech].fields[var]
             raise KeyError(f"unknown mechanism {mech!r}")
         key = {"g_pas": "g", "e_pas": "e", "delay": "del"}.get(var, var)
         if key not in tab.fields:
             raise KeyError(f"unknown variable {mech}.{var}")
         return tab.fields[key]
+
+
+def lib_par_matrix(g: "CellGroup", name: str) -> np.ndarray:
+    """float64[n, npar] parameter columns of library table ``name`` in the
+    order of the C tables (LIB_FIELDS, then ca_ion's nernst flag as 0/1);
+    an absent table gives shape (0, npar)."""
+    cols = list(LIB_FIELDS[name])
+    tab = g.lib.get(name)
+    n = tab.n if tab is not None else 0
+    npar = len(cols) + (1 if name == "ca_ion" else 0)
+    out = np.zeros((n, npar))
+    if n:
+        for c, k in enumerate(cols):
+            out[:, c] = tab.fields[k]
+        if name == "ca_ion":
+            out[:, -1] = tab.ifields["nernst"] != 0
+    return out
+
+
+# states per library table, in the order the forward keeps them
+LIB_STATES = {"ca_ion": ("cai",), "Ca_HVA": ("m", "h"), "Ca_LVAst": ("m", "h"), "Im": ("m",), "K_Pst": ("m", "h"),
+              "K_Tst": ("m", "h"), "NaTg": ("m", "h"), "Nap_Et2": ("m", "h"), "SK_E2": ("z",), "SKv3_1": ("m",)}
 
 
 def empty_table(names, inames=()) -> MechTable:
@@ -325,6 +420,19 @@ def concat_groups(groups, name: str = "group") -> CellGroup:
     hh = cat_tab("hh", ("gnabar", "gkbar", "gl", "el", "ena", "ek"))
     pas = cat_tab("pas", ("g", "e"))
     ic = cat_tab("iclamp", ("del", "dur", "amp"))
+    lib = {}
+    for nm in LIB_NAMES:
+        parts = [(g.lib[nm], m) for g, m in zip(groups, maps) if nm in g.lib]
+        if not parts:
+            continue
+        nodes = np.concatenate([m[t.nodes] for t, m in parts])
+        order = np.argsort(nodes, kind="stable")
+        t0 = parts[0][0]
+        lib[nm] = MechTable(
+            _i32(nodes[order]),
+            {k: _f64(np.concatenate([t.fields[k] for t, _ in parts])[order]) for k in t0.fields},
+            {k: _i32(np.concatenate([t.ifields[k] for t, _ in parts])[order]) for k in t0.ifields},
+        )
     g0 = groups[0]
     out = CellGroup(
         ncell=ncell,
@@ -340,6 +448,7 @@ def concat_groups(groups, name: str = "group") -> CellGroup:
         dt=g0.dt,
         v_init=g0.v_init,
         name=name,
+        lib=lib,
     )
     out.validate()
     return out

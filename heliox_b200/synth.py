@@ -26,7 +26,7 @@ from typing import List, Tuple
 
 import numpy as np
 
-from .model import CellGroup, MechTable, _f64, _i32, concat_groups
+from .model import LIB_FIELDS, LIB_IONS, LIB_NAMES, CellGroup, MechTable, _f64, _i32, concat_groups
 
 RA = 100.0  # Ohm*cm
 HH_STD = dict(gnabar=0.12, gkbar=0.036, gl=3e-4, el=-54.3, ena=50.0, ek=-77.0)
@@ -224,6 +224,101 @@ def giant_cell(ncomp: int = 50000, max_levels: int = 40, seed: int = 7) -> CellG
     g = random_tree_cell(seed, ncomp=ncomp, max_levels=max_levels, seg_len=10.0, amp=0.5)
     g.name = f"giant{ncomp}"
     return g
+
+
+# ---------------------------------------------------------------- library cells
+# Channel densities (S/cm^2) of the user-mech channel set per region
+# (soma, axon initial segment, dendrites), in the range of published layer-5
+# pyramidal-cell fits; the ion parameters are the reference's ion defaults
+# (eion.cuh:306-327) with ena 50, ek -85 and eca from the Nernst equation.
+LIB_DENSITY = {
+    "NaTg": (1.5, 3.0, 0.02),
+    "Nap_Et2": (0.002, 0.006, 0.0),
+    "K_Pst": (0.05, 0.9, 0.0),
+    "K_Tst": (0.03, 0.08, 0.0),
+    "SKv3_1": (0.3, 1.0, 0.004),
+    "SK_E2": (0.05, 0.01, 0.001),
+    "Im": (0.0, 0.0, 1e-4),
+    "Ca_HVA": (1e-3, 1e-3, 5e-5),
+    "Ca_LVAst": (3e-3, 5e-3, 1e-4),
+}
+LIB_CADYN = (dict(gamma=5e-4, decay=460.0), dict(gamma=5e-4, decay=100.0), dict(gamma=5e-4, decay=80.0))
+LIB_GBAR_FIELD = {nm: LIB_FIELDS[nm][0] for nm in LIB_DENSITY}
+
+
+def lib_tree_cell(seed: int, ncomp: int | None = None, nmin: int = 100, nmax: int = 400,
+                  amp: float | None = None) -> CellGroup:
+    """One seeded random-tree cell carrying the user-mech channel set.
+
+    The morphology is ``random_tree_cell``'s (soma, a 4-compartment axon
+    initial segment, tapering dendrites).  Every compartment gets pas
+    (g 3e-5, e -75); the channels of ``LIB_DENSITY`` go where their region's
+    density is nonzero, scaled by a seeded lognormal factor (sigma 0.1);
+    CaDynamics_E2 sits with the Ca channels (depth 0.1 um, minCai 1e-4 mM);
+    na_ion / k_ion / ca_ion sit on every compartment that a mechanism needs
+    them on (ca_ion: cai 5e-5, cao 2 mM, eca by the Nernst equation each
+    step).  IClamp at the soma, del 5 ms, dur 50 ms, amplitude U[0.2, 1] nA.
+    celsius 34 (the channels' temperature: their rate factors hard-code it).
+    """
+    rng = np.random.default_rng(seed + 7_000_000)
+    base = random_tree_cell(seed, ncomp=ncomp, nmin=nmin, nmax=nmax, amp=amp)
+    n = base.nnode
+    region = np.full(n, 2)
+    region[0] = 0
+    region[1:5] = 1
+    lib = {}
+    need = {"na": np.zeros(n, bool), "k": np.zeros(n, bool), "ca": np.zeros(n, bool)}
+    for nm, dens in LIB_DENSITY.items():
+        d = np.asarray(dens)[region]
+        nodes = np.nonzero(d > 0)[0]
+        gbar = d[nodes] * np.exp(0.1 * rng.standard_normal(nodes.size))
+        f = {LIB_GBAR_FIELD[nm]: _f64(gbar)}
+        if nm == "NaTg":
+            f.update(vshifth=_f64(np.zeros(nodes.size)), vshiftm=_f64(np.zeros(nodes.size)),
+                     slopeh=_f64(np.full(nodes.size, 6.0)), slopem=_f64(np.full(nodes.size, 6.0)))
+        if nm == "SK_E2":
+            f["zTau"] = _f64(np.ones(nodes.size))
+        lib[nm] = MechTable(_i32(nodes), f)
+        for ion in LIB_IONS[nm]:
+            need[ion][nodes] = True
+    ca_nodes = np.nonzero(need["ca"])[0]
+    cad = [LIB_CADYN[r] for r in region[ca_nodes]]
+    lib["CaDynamics_E2"] = MechTable(_i32(ca_nodes), {
+        "gamma": _f64([c["gamma"] for c in cad]), "decay": _f64([c["decay"] for c in cad]),
+        "depth": _f64(np.full(ca_nodes.size, 0.1)), "minCai": _f64(np.full(ca_nodes.size, 1e-4))})
+    na = np.nonzero(need["na"])[0]
+    k = np.nonzero(need["k"])[0]
+    lib["na_ion"] = MechTable(_i32(na), {"ena": _f64(np.full(na.size, 50.0))})
+    lib["k_ion"] = MechTable(_i32(k), {"ek": _f64(np.full(k.size, -85.0))})
+    lib["ca_ion"] = MechTable(_i32(ca_nodes), {"cai": _f64(np.full(ca_nodes.size, 5e-5)),
+                                               "cao": _f64(np.full(ca_nodes.size, 2.0)),
+                                               "eca": _f64(np.full(ca_nodes.size, 132.5))},
+                              {"nernst": _i32(np.ones(ca_nodes.size))})
+    g = CellGroup(ncell=1, parent=base.parent, a=base.a, b=base.b, area=base.area, cm=base.cm,
+                  hh=MechTable(_i32([]), {k2: _f64([]) for k2 in HH_STD}),
+                  pas=MechTable(_i32(np.arange(n)), {"g": _f64(np.full(n, 3e-5)), "e": _f64(np.full(n, -75.0))}),
+                  iclamp=base.iclamp, celsius=34.0, v_init=-75.0, name=f"libtree{seed}",
+                  lib={nm: lib[nm] for nm in LIB_NAMES if nm in lib and lib[nm].n})
+    g.validate()
+    return g
+
+
+def lib_tree_batch(ncell: int = 64, seed0: int = 51000, **kw) -> CellGroup:
+    """``ncell`` seeded library cells (seed ``seed0 + cell``) in one group."""
+    g = concat_groups([lib_tree_cell(seed0 + c, **kw) for c in range(ncell)], name=f"libtrees{ncell}")
+    g.v_init = -75.0
+    return g
+
+
+def perturb_lib(g: CellGroup, sigma: float = 0.2, seed: int = 98) -> CellGroup:
+    """Teacher copy: every library channel density multiplied by exp(sigma*N(0,1))."""
+    rng = np.random.default_rng(seed)
+    t = g.copy()
+    for nm, key in LIB_GBAR_FIELD.items():
+        if nm in t.lib:
+            v = t.lib[nm].fields[key]
+            t.lib[nm].fields[key] = _f64(v * np.exp(sigma * rng.standard_normal(v.size)))
+    return t
 
 
 # ---------------------------------------------------------------- teachers

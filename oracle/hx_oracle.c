@@ -29,6 +29,7 @@
  * that crosses no threshold).
  */
 #include "hx_oracle.h"
+#include "hx_oracle_lib.h"
 
 #include <math.h>
 #include <stdint.h>
@@ -232,6 +233,7 @@ typedef struct {
     int rec_step; /* step whose deliveries are being recorded, -1 = off */
     int* ev;      /* pairs (step, synapse) */
     int nev, capev;
+    struct hxo_libstate* lib; /* library mechanisms (hx_oracle_lib.c) */
 } hxo_state;
 
 static int grow(void** p, int* cap, int need, size_t el) {
@@ -256,6 +258,7 @@ static int state_alloc(const hxo_group* g, hxo_state* s) {
     s->n = (double*)calloc(nh, sizeof(double));
     s->rec_step = -1;
     if (!(s->v && s->rhs && s->d && s->m && s->h && s->n)) return -1;
+    if (hxo_lib_alloc(g, &s->lib)) return -1;
     const hxo_net* N = g->net;
     if (N) {
         s->nsyn = N->nexp + N->nexp2;
@@ -311,6 +314,7 @@ static void state_free(hxo_state* s) {
     free(s->gr_k);
     free(s->gr_erev);
     free(s->ev);
+    hxo_lib_free(s->lib);
 }
 
 /* ---------------------------------------------------------------- network */
@@ -521,6 +525,7 @@ static void finitialize(const hxo_group* g, hxo_state* s, double v_init) {
         s->h[j] = r.hinf;
         s->n[j] = r.ninf;
     }
+    hxo_lib_init(g, s->lib, s->v);
     if (!N) return;
     for (int j = 0; j < N->nexp; j++) s->sA[j] = s->sB[j] = 0.0;
     for (int q = 0; q < N->nexp2; q++) {
@@ -647,6 +652,8 @@ static void setup_tree_matrix(const hxo_group* g, hxo_state* s) {
             pp_add(rhs, d, i, aw * (gs * ((v[i] + FD_EPS) - er)), aw * (gs * (v[i] - er)), g->area[i], 0);
         }
     }
+    /* library mechanisms (types after the network mechanisms) */
+    hxo_lib_current(g, s->lib, v, rhs, d);
     /* cap_jacob_cpu, capac.cpp:68-78 with cj = 1/dt */
     {
         double cj = 1.0 / g->dt;
@@ -700,6 +707,8 @@ static void solve_serial_T(const hxo_group* g, double* d, double* rhs) {
 /* nonvint_cpu, simulate.cpp:784-852: states at the updated v */
 static void nonvint(const hxo_group* g, hxo_state* s) {
     const double dt = g->dt;
+    hxo_lib_state_ion(g, s->lib); /* mech_write_state_ion_list first */
+    hxo_lib_state(g, s->lib, s->v);
     for (int j = 0; j < g->nhh; j++) {
         hh_rates_t r;
         hh_rates(s->v[g->hh_node[j]], g->celsius, &r);
@@ -768,6 +777,25 @@ int hxo_forward(const hxo_group* g, double v_init, int nstep, int nprobe, const 
     return 0;
 }
 
+int hxo_forward_lib(const hxo_group* g, double v_init, int nstep, int nprobe, const int* probe, double* trace,
+                    double* lib_final, int nlib_final) {
+    hxo_state s;
+    if (g->net) g->net->nspike = g->net->ns_nspike = 0;
+    if (state_alloc(g, &s)) {
+        state_free(&s);
+        return -1;
+    }
+    finitialize(g, &s, v_init);
+    if (trace) record(g, &s, nprobe, probe, trace);
+    for (int k = 0; k < nstep; k++) {
+        fadvance(g, &s);
+        if (trace) record(g, &s, nprobe, probe, trace + (size_t)(k + 1) * nprobe);
+    }
+    int rc = lib_final ? hxo_lib_final(g, s.lib, lib_final, nlib_final) : 0;
+    state_free(&s);
+    return rc < 0 ? rc : 0;
+}
+
 /* ---------------------------------------------------------------- adjoint */
 static void zero_if(double* p, int n) {
     if (p && n > 0) memset(p, 0, sizeof(double) * (size_t)n);
@@ -780,6 +808,7 @@ static void zero_if(double* p, int n) {
 
 int hxo_adjoint(const hxo_group* g, double v_init, int nstep, int nprobe, const int* probe, const double* dLdv,
                 double* trace, hxo_grads* gr) {
+    if (g->lib) return -2; /* library mechanisms: gradients are checked by finite differences */
     const int nn = g->nnode, nh = g->nhh;
     hxo_net* N = g->net;
     const int nsyn = N ? N->nexp + N->nexp2 : 0, ngr = N ? N->ngr : 0;

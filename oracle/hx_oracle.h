@@ -56,6 +56,27 @@ typedef struct hxo_net {
     int ns_nspike;
 } hxo_net;
 
+/* Library mechanisms (optional; hxo_group.lib may be NULL): the ions and the
+ * user-mech channel set, CoreNEURON types after the network mechanisms in
+ * this order.  Table t holds n instances on sorted, distinct nodes; par holds
+ * HXO_LIB_NPAR columns per instance (row-major):
+ *   na_ion: ena | k_ion: ek | ca_ion: cai (initial), cao, eca, nernst (0/1)
+ *   CaDynamics_E2: gamma, decay, depth, minCai
+ *   Ca_HVA, Ca_LVAst, Im, K_Pst, K_Tst, Nap_Et2, SKv3_1: gbar
+ *   NaTg: gbar, vshifth, vshiftm, slopeh, slopem | SK_E2: gbar, zTau */
+enum {
+    HXO_NA_ION = 0, HXO_K_ION, HXO_CA_ION, HXO_CADYN, HXO_CA_HVA, HXO_CA_LVAST, HXO_IM, HXO_K_PST, HXO_K_TST,
+    HXO_NATG, HXO_NAP_ET2, HXO_SK_E2, HXO_SKV3_1, HXO_LIB_NTYPE
+};
+typedef struct hxo_lib_table {
+    int n;
+    const int* node;
+    const double* par;
+} hxo_lib_table;
+typedef struct hxo_lib {
+    hxo_lib_table t[HXO_LIB_NTYPE];
+} hxo_lib;
+
 typedef struct hxo_group {
     int ncell, nnode;
     const int* parent;            /* -1 for the ncell roots, parent[i] < i otherwise */
@@ -71,6 +92,7 @@ typedef struct hxo_group {
     const int* ic_node;
     const double *ic_del, *ic_dur, *ic_amp;
     hxo_net* net;
+    const hxo_lib* lib;
 } hxo_group;
 
 /* Gradient outputs; any pointer may be NULL.  Each array is per instance of its
@@ -90,7 +112,14 @@ typedef struct hxo_grads {
 int hxo_forward(const hxo_group* g, double v_init, int nstep, int nprobe, const int* probe,
                 double* trace, double* v_final, double* m_final, double* h_final, double* n_final);
 
-/* Forward + reverse sweep.  dLdv: (nstep+1) x nprobe, dL/d(trace).  The trace of
+/* Forward that also returns the library states after the last step: for
+ * every table t in type order, its instances' states (Ca_HVA, Ca_LVAst,
+ * K_Pst, K_Tst, NaTg, Nap_Et2: m, h; Im, SKv3_1: m; SK_E2: z; ca_ion: cai)
+ * appended to lib_final (nlib_final doubles available; -2 if too small). */
+int hxo_forward_lib(const hxo_group* g, double v_init, int nstep, int nprobe, const int* probe, double* trace,
+                    double* lib_final, int nlib_final);
+
+/* Forward + reverse sweep (groups without library mechanisms; -2 otherwise).  dLdv: (nstep+1) x nprobe, dL/d(trace).  The trace of
  * the forward is written to trace (may be NULL). */
 int hxo_adjoint(const hxo_group* g, double v_init, int nstep, int nprobe, const int* probe,
                 const double* dLdv, double* trace, hxo_grads* grads);

@@ -1,0 +1,390 @@
+/*
+ * hx_oracle_lib.c -- TEST INFRASTRUCTURE ONLY (see hx_oracle.h).
+ *
+ * The library mechanisms of the CPU oracle, restated in plain C in the
+ * expression order of the reference's own files:
+ *   ions (erev, Nernst, current reset)   src/mech/eion.cuh:38-56, 155-197
+ *   CaDynamics_E2                        src/mech/user-mech/CaDynamics_E2.cu:78-137
+ *   Ca_HVA                               src/mech/user-mech/CA_HVA.cu (vtrap, rates,
+ *                                        current, state)
+ *   Ca_LVAst                             src/mech/user-mech/Ca_LVAst.cu
+ *   Im                                   src/mech/user-mech/Im.cu
+ *   K_Pst, K_Tst                         src/mech/user-mech/K_Pst.cu, K_Tst.cu
+ *   NaTg                                 src/mech/user-mech/NaTg.cu:78-160
+ *   Nap_Et2                              src/mech/user-mech/Nap_Et2.cu
+ *   SK_E2                                src/mech/user-mech/SK_E2.cu:70-132
+ *   SKv3_1                               src/mech/user-mech/SKv3_1.cu
+ * through MechTemp's finite-difference current (mech_template.cuh:589-648)
+ * and the state phase order of nonvint_cpu (simulate.cpp:784-852: mechanisms
+ * that write an ion in their state update first, then the others in type
+ * order).  Mechanism types follow the network mechanisms, in the order of the
+ * hxo_lib tables.
+ */
+#include <math.h>
+#include <stdlib.h>
+#include <string.h>
+
+#include "hx_oracle.h"
+#include "hx_oracle_lib.h"
+
+#define FD_EPS 0.001
+
+static const int NPAR[HXO_LIB_NTYPE] = {1, 1, 4, 4, 1, 1, 1, 1, 1, 5, 1, 2, 1};
+static const int NST[HXO_LIB_NTYPE] = {0, 0, 0, 0, 2, 2, 1, 2, 2, 2, 2, 1, 1};
+
+struct hxo_libstate {
+    double* st[HXO_LIB_NTYPE]; /* n x NST per table */
+    double *cai, *eca, *ica;   /* per ca_ion instance */
+    double *ena, *ek;          /* per na_ion / k_ion instance */
+    int *na_of, *k_of, *ca_of; /* node -> ion instance, -1 if none */
+};
+
+/* units.h:18-24 (2018 CODATA) and eion.cuh:38-56 */
+static const double kFaraday = 1.602176634e-19 * 6.02214076e+23;
+static const double kGas = 1.380649e-23 * 6.02214076e+23;
+
+static double ktf(double celsius) { return 1000. * kGas * (celsius + 273.15) / kFaraday; }
+
+static double nernst(double ci, double co, double z, double celsius) {
+    if (z == 0) return 0.;
+    if (ci <= 0.) return 1e6;
+    if (co <= 0.) return -1e6;
+    return ktf(celsius) / z * log(co / ci);
+}
+
+static double qt23(void) { return pow(2.3, ((34.0 - 21.0) / 10.0)); }
+
+/* cnexp update of NaTg, Nap_Et2, SKv3_1, SK_E2, Im, K_Pst, K_Tst, Ca_LVAst */
+static double cnexp(double x, double inf, double tau, double dt) {
+    return x + (1.0 - exp(dt * (-1.0 / tau))) * (-(inf / tau) / (-1.0 / tau) - x);
+}
+
+/* ------------------------------------------------------------------ rates */
+static void natg_rates(double v, const double* p, double r[4]) {
+    const double qt = qt23();
+    const double vshifth = p[1], vshiftm = p[2], slopeh = p[3], slopem = p[4];
+    double v_m = v;
+    if (v_m == -38.0) v_m = v_m + 0.0001;
+    const double mA = (0.182 * (v_m - (-38.0 + vshiftm))) / (1.0 - exp(-(v_m - (-38.0 + vshiftm)) / slopem));
+    const double mB = (0.124 * (-v_m + (-38.0 + vshiftm))) / (1.0 - exp(-(-v_m + (-38.0 + vshiftm)) / slopem));
+    r[1] = (1.0 / (mA + mB)) / qt;
+    r[0] = mA / (mA + mB);
+    double v_h = v;
+    if (v_h == -66.0) v_h = v_h + 0.0001;
+    const double hA = (-0.015 * (v_h - (-66.0 + vshifth))) / (1.0 - exp((v_h - (-66.0 + vshifth)) / slopeh));
+    const double hB = (-0.015 * (-v_h + (-66.0 + vshifth))) / (1.0 - exp((-v_h + (-66.0 + vshifth)) / slopeh));
+    r[3] = (1.0 / (hA + hB)) / qt;
+    r[2] = hA / (hA + hB);
+}
+
+static void nap_rates(double v, double r[4]) {
+    const double qt = qt23();
+    r[0] = 1.0 / (1.0 + exp((v - (-52.6)) / (-4.6)));
+    double v_m = v;
+    if (v_m == -38.0) v_m = v_m + 0.0001;
+    const double mA = (0.182 * (v_m - (-38.0))) / (1.0 - exp(-(v_m - (-38.0)) / 6.0));
+    const double mB = (0.124 * (-v_m - 38.0)) / (1.0 - exp(-(-v_m - 38.0) / 6.0));
+    r[1] = 6.0 * (1.0 / (mA + mB)) / qt;
+    double v_h1 = v;
+    if (v_h1 == -17.0) v_h1 = v_h1 + 0.0001;
+    double v_h2 = v;
+    if (v_h2 == -64.4) v_h2 = v_h2 + 0.0001;
+    r[2] = 1.0 / (1.0 + exp((v - (-48.8)) / 10.0));
+    const double hA = -2.88e-6 * (v_h1 + 17.0) / (1.0 - exp((v_h1 + 17.0) / 4.63));
+    const double hB = 6.94e-6 * (v_h2 + 64.4) / (1.0 - exp(-(v_h2 + 64.4) / 2.63));
+    r[3] = (1.0 / (hA + hB)) / qt;
+}
+
+static void kpst_rates(double v_param, double r[4]) {
+    const double qt = qt23();
+    const double v = v_param + 10.0;
+    r[0] = (1.0 / (1.0 + exp(-(v + 1.0) / 12.0)));
+    if (v < -50.0)
+        r[1] = (1.25 + 175.03 * exp(-v * (-0.026))) / qt;
+    else
+        r[1] = ((1.25 + 13.0 * exp(-v * 0.026))) / qt;
+    r[2] = 1.0 / (1.0 + exp(-(v + 54.0) / (-11.0)));
+    r[3] = (360.0 + (1010.0 + 24.0 * (v + 55.0)) * exp(-pow(((v + 75.0) / 48.0), 2.0))) / qt;
+}
+
+static void ktst_rates(double v_param, double r[4]) {
+    const double qt = qt23();
+    const double v = v_param + 10.0;
+    r[0] = 1.0 / (1.0 + exp(-(v + 0.0) / 19.0));
+    r[1] = (0.34 + 0.92 * exp(-pow(((v + 71.0) / 59.0), 2.0))) / qt;
+    r[2] = 1.0 / (1.0 + exp(-(v + 66.0) / (-10.0)));
+    r[3] = (8.0 + 49.0 * exp(-pow(((v + 73.0) / 23.0), 2.0))) / qt;
+}
+
+static void calva_rates(double v_param, double r[4]) {
+    const double qt = qt23();
+    const double v = v_param + 10.0;
+    r[0] = 1.0 / (1.0 + exp((v - (-30.0)) / (-6.0)));
+    r[1] = (5.0 + 20.0 / (1.0 + exp((v - (-25.0)) / 5.0))) / qt;
+    r[2] = 1.0 / (1.0 + exp((v - (-80.0)) / 6.4));
+    r[3] = (20.0 + 50.0 / (1.0 + exp((v - (-40.0)) / 7.0))) / qt;
+}
+
+static double cahva_vtrap(double x, double y) {
+    if (fabs(x / y) < 1e-6) return y * (1.0 - x / y / 2.0);
+    return x / (exp(x / y) - 1.0);
+}
+
+static void cahva_rates(double v, double r[4]) {
+    const double mA = 0.055 * cahva_vtrap(-27.0 - v, 3.8);
+    const double mB = 0.94 * exp((-75.0 - v) / 17.0);
+    r[0] = mA / (mA + mB);
+    r[1] = 1.0 / (mA + mB);
+    const double hA = 0.000457 * exp((-13.0 - v) / 50.0);
+    const double hB = 0.0065 / (exp((-v - 15.0) / 28.0) + 1.0);
+    r[2] = hA / (hA + hB);
+    r[3] = 1.0 / (hA + hB);
+}
+
+static void im_rates(double v, double r[2]) {
+    const double qt = qt23();
+    const double mA = 3.3e-3 * exp(2.5 * 0.04 * (v - (-35.0)));
+    const double mB = 3.3e-3 * exp(-2.5 * 0.04 * (v - (-35.0)));
+    r[0] = mA / (mA + mB);
+    r[1] = (1.0 / (mA + mB)) / qt;
+}
+
+static void skv31_rates(double v, double r[2]) {
+    r[0] = 1.0 / (1.0 + exp((v - 18.700) / (-9.700)));
+    r[1] = 0.2 * 20.0 / (1.0 + exp((v - (-46.560)) / (-44.140)));
+}
+
+static double sk_zinf(double ca) {
+    double ca_safe = ca;
+    if (ca_safe < 1e-7) ca_safe = ca_safe + 1e-07;
+    return 1.0 / (1.0 + pow((0.00043 / ca_safe), 4.8));
+}
+
+/* ------------------------------------------------------------------ current */
+/* I(v) of one channel instance (the value current_single_node returns) */
+static double chan_current(int t, double v, const double* p, const double* s, double erev) {
+    switch (t) {
+        case HXO_CA_HVA: {
+            const double g = p[0] * s[0] * s[0] * s[1];
+            return g * (v - erev);
+        }
+        case HXO_CA_LVAST:
+        case HXO_K_PST:
+            return p[0] * s[0] * s[0] * s[1] * (v - erev);
+        case HXO_K_TST:
+            return p[0] * pow(s[0], 4.0) * s[1] * (v - erev);
+        case HXO_NATG:
+        case HXO_NAP_ET2:
+            return p[0] * s[0] * s[0] * s[0] * s[1] * (v - erev);
+        case HXO_IM:
+        case HXO_SKV3_1:
+        case HXO_SK_E2:
+            return p[0] * s[0] * (v - erev);
+        default:
+            return 0.0;
+    }
+}
+
+/* 0: na, 1: k, 2: ca (the ion whose erev a channel reads and current it writes) */
+static int chan_ion(int t) {
+    switch (t) {
+        case HXO_NATG:
+        case HXO_NAP_ET2:
+            return 0;
+        case HXO_CA_HVA:
+        case HXO_CA_LVAST:
+            return 2;
+        default:
+            return 1;
+    }
+}
+
+/* ------------------------------------------------------------------ lifecycle */
+int hxo_lib_alloc(const hxo_group* g, struct hxo_libstate** out) {
+    *out = NULL;
+    if (!g->lib) return 0;
+    struct hxo_libstate* L = (struct hxo_libstate*)calloc(1, sizeof(*L));
+    if (!L) return -1;
+    *out = L;
+    const hxo_lib* lib = g->lib;
+    for (int t = 0; t < HXO_LIB_NTYPE; t++) {
+        L->st[t] = (double*)calloc((size_t)(lib->t[t].n * NST[t] + 1), sizeof(double));
+        if (!L->st[t]) return -1;
+    }
+    const int nca = lib->t[HXO_CA_ION].n + 1;
+    L->cai = (double*)calloc((size_t)nca, sizeof(double));
+    L->eca = (double*)calloc((size_t)nca, sizeof(double));
+    L->ica = (double*)calloc((size_t)nca, sizeof(double));
+    L->ena = (double*)calloc((size_t)lib->t[HXO_NA_ION].n + 1, sizeof(double));
+    L->ek = (double*)calloc((size_t)lib->t[HXO_K_ION].n + 1, sizeof(double));
+    L->na_of = (int*)malloc(sizeof(int) * (size_t)g->nnode);
+    L->k_of = (int*)malloc(sizeof(int) * (size_t)g->nnode);
+    L->ca_of = (int*)malloc(sizeof(int) * (size_t)g->nnode);
+    if (!(L->cai && L->eca && L->ica && L->ena && L->ek && L->na_of && L->k_of && L->ca_of)) return -1;
+    for (int i = 0; i < g->nnode; i++) L->na_of[i] = L->k_of[i] = L->ca_of[i] = -1;
+    for (int j = 0; j < lib->t[HXO_NA_ION].n; j++) L->na_of[lib->t[HXO_NA_ION].node[j]] = j;
+    for (int j = 0; j < lib->t[HXO_K_ION].n; j++) L->k_of[lib->t[HXO_K_ION].node[j]] = j;
+    for (int j = 0; j < lib->t[HXO_CA_ION].n; j++) L->ca_of[lib->t[HXO_CA_ION].node[j]] = j;
+    return 0;
+}
+
+void hxo_lib_free(struct hxo_libstate* L) {
+    if (!L) return;
+    for (int t = 0; t < HXO_LIB_NTYPE; t++) free(L->st[t]);
+    free(L->cai);
+    free(L->eca);
+    free(L->ica);
+    free(L->ena);
+    free(L->ek);
+    free(L->na_of);
+    free(L->k_of);
+    free(L->ca_of);
+    free(L);
+}
+
+/* erev / concentration an instance at node i reads */
+static double ion_erev(const struct hxo_libstate* L, int ion, int i) {
+    if (ion == 0) return L->ena[L->na_of[i]];
+    if (ion == 1) return L->ek[L->k_of[i]];
+    return L->eca[L->ca_of[i]];
+}
+
+/* finitialize: INITIAL blocks in type order (ions first; iontype flags:
+ * na / k 0, ca 040|0100 when nernst else 0, eion.cuh:170-186) */
+void hxo_lib_init(const hxo_group* g, struct hxo_libstate* L, const double* v) {
+    if (!L) return;
+    const hxo_lib* lib = g->lib;
+    for (int j = 0; j < lib->t[HXO_NA_ION].n; j++) L->ena[j] = lib->t[HXO_NA_ION].par[j];
+    for (int j = 0; j < lib->t[HXO_K_ION].n; j++) L->ek[j] = lib->t[HXO_K_ION].par[j];
+    for (int j = 0; j < lib->t[HXO_CA_ION].n; j++) {
+        const double* p = lib->t[HXO_CA_ION].par + 4 * j;
+        L->cai[j] = p[0];
+        L->eca[j] = p[3] != 0.0 ? nernst(p[0], p[1], 2.0, g->celsius) : p[2];
+        L->ica[j] = 0.0;
+    }
+    for (int t = HXO_CA_HVA; t < HXO_LIB_NTYPE; t++) {
+        const hxo_lib_table* T = &lib->t[t];
+        for (int j = 0; j < T->n; j++) {
+            const int i = T->node[j];
+            const double* p = T->par + NPAR[t] * j;
+            double* s = L->st[t] + NST[t] * j;
+            double r[4] = {0.0, 0.0, 0.0, 0.0};
+            switch (t) {
+                case HXO_CA_HVA: cahva_rates(v[i], r); break;
+                case HXO_CA_LVAST: calva_rates(v[i], r); break;
+                case HXO_K_PST: kpst_rates(v[i], r); break;
+                case HXO_K_TST: ktst_rates(v[i], r); break;
+                case HXO_NATG: natg_rates(v[i], p, r); break;
+                case HXO_NAP_ET2: nap_rates(v[i], r); break;
+                case HXO_IM: im_rates(v[i], r); break;
+                case HXO_SKV3_1: skv31_rates(v[i], r); break;
+                case HXO_SK_E2: r[0] = sk_zinf(L->cai[L->ca_of[i]]); break;
+            }
+            s[0] = r[0];
+            if (NST[t] == 2) s[1] = r[2];
+        }
+    }
+}
+
+/* current phase: ion mechanisms (cur = 0, Nernst erev) then the channels in
+ * type order, each through the FD conductance of MechTemp::current_cpu */
+void hxo_lib_current(const hxo_group* g, struct hxo_libstate* L, const double* v, double* rhs, double* d) {
+    if (!L) return;
+    const hxo_lib* lib = g->lib;
+    for (int j = 0; j < lib->t[HXO_CA_ION].n; j++) {
+        const double* p = lib->t[HXO_CA_ION].par + 4 * j;
+        L->ica[j] = 0.0;
+        if (p[3] != 0.0) L->eca[j] = nernst(L->cai[j], p[1], 2.0, g->celsius);
+    }
+    for (int t = HXO_CA_HVA; t < HXO_LIB_NTYPE; t++) {
+        const hxo_lib_table* T = &lib->t[t];
+        const int ion = chan_ion(t);
+        for (int j = 0; j < T->n; j++) {
+            const int i = T->node[j];
+            const double* p = T->par + NPAR[t] * j;
+            const double* s = L->st[t] + NST[t] * j;
+            const double e = ion_erev(L, ion, i);
+            double gg = chan_current(t, v[i] + 0.001, p, s, e);
+            const double r = chan_current(t, v[i], p, s, e);
+            if (ion == 2) L->ica[L->ca_of[i]] += r;
+            gg = (gg - r) / FD_EPS;
+            rhs[i] -= r;
+            d[i] += gg;
+        }
+    }
+}
+
+/* state phase, part 1: mechanisms that write an ion in their state update
+ * (CaDynamics_E2) */
+void hxo_lib_state_ion(const hxo_group* g, struct hxo_libstate* L) {
+    if (!L) return;
+    const hxo_lib_table* T = &g->lib->t[HXO_CADYN];
+    const double dt = g->dt;
+    for (int j = 0; j < T->n; j++) {
+        const int c = L->ca_of[T->node[j]];
+        const double* p = T->par + 4 * j;
+        const double FARADAY = 96485.3321233100184;
+        const double gamma_val = p[0], decay_val = p[1], depth_val = p[2], minCai_val = p[3];
+        const double ica_val = L->ica[c], cai_val = L->cai[c];
+        const double drive_ica = -(10000.0) * (ica_val * gamma_val) / (2.0 * FARADAY * depth_val);
+        const double exp_factor = exp(dt * (-1.0 / decay_val));
+        const double steady_term = -(drive_ica - (-minCai_val) / decay_val) / (-1.0 / decay_val);
+        L->cai[c] = cai_val + (1.0 - exp_factor) * (steady_term - cai_val);
+    }
+}
+
+/* state phase, part 2: the channels in type order at the updated v */
+void hxo_lib_state(const hxo_group* g, struct hxo_libstate* L, const double* v) {
+    if (!L) return;
+    const hxo_lib* lib = g->lib;
+    const double dt = g->dt;
+    for (int t = HXO_CA_HVA; t < HXO_LIB_NTYPE; t++) {
+        const hxo_lib_table* T = &lib->t[t];
+        for (int j = 0; j < T->n; j++) {
+            const int i = T->node[j];
+            const double* p = T->par + NPAR[t] * j;
+            double* s = L->st[t] + NST[t] * j;
+            double r[4] = {0.0, 0.0, 0.0, 0.0};
+            if (t == HXO_CA_HVA) {
+                cahva_rates(v[i], r);
+                s[0] = s[0] + (1.0 - exp(-dt / r[1])) * (r[0] - s[0]);
+                s[1] = s[1] + (1.0 - exp(-dt / r[3])) * (r[2] - s[1]);
+                continue;
+            }
+            if (t == HXO_SK_E2) {
+                const double zTau = p[1];
+                s[0] = cnexp(s[0], sk_zinf(L->cai[L->ca_of[i]]), zTau, dt);
+                continue;
+            }
+            switch (t) {
+                case HXO_CA_LVAST: calva_rates(v[i], r); break;
+                case HXO_K_PST: kpst_rates(v[i], r); break;
+                case HXO_K_TST: ktst_rates(v[i], r); break;
+                case HXO_NATG: natg_rates(v[i], p, r); break;
+                case HXO_NAP_ET2: nap_rates(v[i], r); break;
+                case HXO_IM: im_rates(v[i], r); break;
+                case HXO_SKV3_1: skv31_rates(v[i], r); break;
+            }
+            s[0] = cnexp(s[0], r[0], r[1], dt);
+            if (NST[t] == 2) s[1] = cnexp(s[1], r[2], r[3], dt);
+        }
+    }
+}
+
+int hxo_lib_final(const hxo_group* g, const struct hxo_libstate* L, double* out, int cap) {
+    if (!L) return 0;
+    int k = 0;
+    for (int t = 0; t < HXO_LIB_NTYPE; t++) {
+        const int n = g->lib->t[t].n;
+        if (t == HXO_CA_ION) {
+            if (k + n > cap) return -2;
+            memcpy(out + k, L->cai, sizeof(double) * (size_t)n);
+            k += n;
+        } else if (NST[t]) {
+            if (k + n * NST[t] > cap) return -2;
+            memcpy(out + k, L->st[t], sizeof(double) * (size_t)(n * NST[t]));
+            k += n * NST[t];
+        }
+    }
+    return k;
+}

@@ -38,6 +38,14 @@ class _Net(C.Structure):
     ]
 
 
+class _LibTable(C.Structure):
+    _fields_ = [("n", C.c_int), ("node", _ip), ("par", _dp)]
+
+
+class _Lib(C.Structure):
+    _fields_ = [("t", _LibTable * 13)]
+
+
 class _Group(C.Structure):
     _fields_ = [
         ("ncell", C.c_int),
@@ -67,6 +75,7 @@ class _Group(C.Structure):
         ("ic_dur", _dp),
         ("ic_amp", _dp),
         ("net", C.POINTER(_Net)),
+        ("lib", C.POINTER(_Lib)),
     ]
 
 
@@ -193,6 +202,8 @@ def lib():
         L.hxo_forward.restype = C.c_int
         L.hxo_adjoint.argtypes = [C.POINTER(_Group), C.c_double, C.c_int, C.c_int, _ip, _dp, _dp, C.POINTER(_Grads)]
         L.hxo_adjoint.restype = C.c_int
+        L.hxo_forward_lib.argtypes = [C.POINTER(_Group), C.c_double, C.c_int, C.c_int, _ip, _dp, _dp, C.c_int]
+        L.hxo_forward_lib.restype = C.c_int
         _LIB = L
     return _LIB
 
@@ -274,6 +285,18 @@ class _Bound:
             n.ns_spike_cap, n.ns_spike_id, n.ns_spike_t, n.ns_nspike = cap, _i(self.ns_id), _d(self.ns_t), 0
             self.net = n
             s.net = C.pointer(n)
+        self.lib = None
+        if g.lib:
+            from heliox_b200.model import LIB_NAMES, lib_par_matrix
+
+            lb = _Lib()
+            for t, nm in enumerate(LIB_NAMES):
+                tab = g.lib.get(nm)
+                lb.t[t].n = tab.n if tab is not None else 0
+                lb.t[t].node = I(tab.nodes if tab is not None else np.zeros(0, np.int32))
+                lb.t[t].par = D(lib_par_matrix(g, nm).reshape(-1))
+            self.lib = lb
+            s.lib = C.pointer(lb)
         self.s = s
 
     def netstim_spikes(self):
@@ -306,6 +329,30 @@ def forward(g, nstep: int, probe: Optional[Sequence[int]] = None, v_init: Option
         raise RuntimeError("oracle forward failed")
     return trace, {"v": vf, "m": mf[: g.hh.n], "h": hf[: g.hh.n], "n": nf[: g.hh.n], "spikes": b.spikes(),
                    "netstim_spikes": b.netstim_spikes()}
+
+
+def forward_lib(g, nstep: int, probe: Optional[Sequence[int]] = None, v_init: Optional[float] = None):
+    """Forward of a group with library mechanisms; returns (trace, final
+    library states {"<mech>.<state>": array per instance})."""
+    from heliox_b200.model import LIB_NAMES, LIB_STATES
+
+    L = lib()
+    probe = np.ascontiguousarray(g.soma_nodes() if probe is None else probe, dtype=np.int32)
+    b = _Bound(g)
+    trace = np.zeros((nstep + 1, probe.shape[0]))
+    sizes = [(nm, g.lib[nm].n, LIB_STATES[nm]) for nm in LIB_NAMES if nm in g.lib and nm in LIB_STATES]
+    buf = np.zeros(sum(n * len(st) for _, n, st in sizes) + 1)
+    rc = L.hxo_forward_lib(C.byref(b.s), float(g.v_init if v_init is None else v_init), int(nstep),
+                           int(probe.shape[0]), _i(probe), _d(trace), _d(buf), int(buf.shape[0]))
+    if rc != 0:
+        raise RuntimeError("oracle forward failed")
+    out, k = {}, 0
+    for nm, n, st in sizes:
+        blk = buf[k: k + n * len(st)].reshape(n, len(st))
+        k += n * len(st)
+        for c, sn in enumerate(st):
+            out[f"{nm}.{sn}"] = blk[:, c].copy()
+    return trace, out
 
 
 GRAD_KEYS = ("hh.gnabar", "hh.gkbar", "hh.gl", "hh.el", "pas.g", "pas.e", "cm", "IClamp.amp")

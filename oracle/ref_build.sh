@@ -21,12 +21,16 @@ NVFLAGS="-std=c++20 -O2 -Xcompiler -fPIC,-ffp-contract=off,-fno-fast-math,-w -di
  -gencode arch=compute_100a,code=sm_100a"
 
 # the integrator, its loader and the mechanisms the synthetic configurations use
+# (the library cells add the user-mech channel set and calcium dynamics)
 SRCS=$(cd "$REF" && ls \
   simulate.cpp simulate.cu neuron.cpp permute.cpp permute_order.cpp vecplay.cu \
   io/*.cpp io/*.cu utils/*.cpp utils/*.cu mech/*.cpp mech/*.cu mech/build-in-mech/*.cpp mech/build-in-mech/*.cu \
   spike/*.cpp spike/*.cu spike/postsyn_mech/*.cpp spike/postsyn_mech/*.cu optimizer/*.cpp optimizer/*.cu \
   mech/user-mech/hh_templated.cu mech/user-mech/pas_templated.cu mech/user-mech/iclamp_templated.cu \
   mech/user-mech/HalfGap.cu mech/worm-lr-mech/gapjunction_lr.cu mech/worm-lr-mech/neuron_to_neuron_syn_lr.cu \
+  mech/user-mech/CaDynamics_E2.cu mech/user-mech/CA_HVA.cu mech/user-mech/Ca_LVAst.cu mech/user-mech/Im.cu \
+  mech/user-mech/K_Pst.cu mech/user-mech/K_Tst.cu mech/user-mech/NaTg.cu mech/user-mech/Nap_Et2.cu \
+  mech/user-mech/SK_E2.cu mech/user-mech/SKv3_1.cu \
   2>/dev/null)
 
 compile() {

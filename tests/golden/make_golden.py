@@ -3,7 +3,7 @@
 Needs the reference sources (to build oracle/_ref/hxref_run with
 oracle/ref_build.sh); run from the repository root:
 
-    python tests/golden/make_golden.py
+    python tests/golden/make_golden.py [case ...]
 
 Each case exports a seeded synthetic group in CoreNEURON format
 (heliox_b200.coredat), runs the reference (read_coredat -> data_format_trans ->
@@ -33,7 +33,19 @@ CASES = {
                     2400, None),
     # HalfGap + gapjunction_lr + neuron_to_neuron_syn_lr coupling
     "net_coupled": (lambda: synth.coupled_network(), 2000, None),
+    # user-mech channel set with calcium dynamics (spiking library cells)
+    "lib_cells": (lambda: synth.lib_tree_batch(2, seed0=700, nmax=200), 2000, None),
+    # hh cells and library cells in one group
+    "lib_mixed": (lambda: _lib_mixed(), 1200, None),
 }
+
+
+def _lib_mixed():
+    from heliox_b200.model import concat_groups
+
+    g = concat_groups([synth.lib_tree_cell(11, ncomp=80), synth.random_tree_cell(12, ncomp=90)])
+    g.celsius = 20.0
+    return g
 
 
 ADAM = dict(n=64, steps=25, lr=1e-3, inv_record_steps=0.25, beta1=0.9, beta2=0.999, eps=1e-8, impedance=2.0, seed=5)
@@ -46,20 +58,30 @@ def adam_inputs():
     return w0, grads
 
 
-def main():
+def main(names=None):
+    """Regenerate every fixture, or only the named cases."""
+    if names:
+        for name in names:
+            make_case(name)
+        return
     w0, grads = adam_inputs()
     ws, m, v = O.adam_ref(w0, grads, ADAM["lr"], ADAM["inv_record_steps"], ADAM["beta1"], ADAM["beta2"], ADAM["eps"],
                           ADAM["impedance"])
     np.savez_compressed(os.path.join(HERE, "adam.npz"), w0=w0, grads=grads, weights=ws, m=m, v=v)
     print("adam", ws.shape)
-    for name, (make, nstep, probes) in CASES.items():
-        g = make()
-        p = np.asarray(probes if probes is not None else list(g.soma_nodes()) + [g.nnode - 1], dtype=np.int32)
-        tr, spk = O.ref_forward(g, nstep, probe=p)
-        np.savez_compressed(os.path.join(HERE, f"{name}.npz"), trace=tr, probes=p, nstep=nstep,
-                            spikes=np.asarray(spk, dtype=np.float64).reshape(-1, 2))
-        print(name, tr.shape, len(spk))
+    for name in CASES:
+        make_case(name)
+
+
+def make_case(name):
+    make, nstep, probes = CASES[name]
+    g = make()
+    p = np.asarray(probes if probes is not None else list(g.soma_nodes()) + [g.nnode - 1], dtype=np.int32)
+    tr, spk = O.ref_forward(g, nstep, probe=p)
+    np.savez_compressed(os.path.join(HERE, f"{name}.npz"), trace=tr, probes=p, nstep=nstep,
+                        spikes=np.asarray(spk, dtype=np.float64).reshape(-1, 2))
+    print(name, tr.shape, len(spk))
 
 
 if __name__ == "__main__":
-    main()
+    main(sys.argv[1:])

@@ -150,3 +150,17 @@ def test_network_adjoint_vs_fd_of_reference_forward():
                 vals.append(L(gg))
             fd = (-vals[0] + 8 * vals[1] - 8 * vals[2] + vals[3]) / (12 * h)
             assert abs(gr[key][j] - fd) <= 1e-6 * abs(fd), (key, gr[key][j], fd)
+
+
+@needs_ref
+@pytest.mark.parametrize("seed", [1, 2])
+def test_oracle_library_cells_bit_exact_vs_reference_live(seed):
+    """The user-mech channel set, ions and calcium dynamics (library cells and
+    a teacher with perturbed channel densities) against the reference."""
+    g = synth.lib_tree_batch(2, seed0=3000 + seed, nmax=180)
+    teacher = synth.perturb_lib(g, 0.3, seed=seed)
+    for grp in (g, teacher):
+        probe = np.array(list(grp.soma_nodes()) + [grp.nnode - 1], dtype=np.int32)
+        tr, _ = O.forward(grp, 1600, probe=probe)
+        ref, _ = O.ref_forward(grp, 1600, probe=probe)
+        assert np.array_equal(tr, ref), np.max(np.abs(tr - ref))
