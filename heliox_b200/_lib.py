@@ -34,8 +34,30 @@ HX_P = {
     "gapjunction_lr.g": 13,
     "gapjunction_lr.w": 14,
     "neuron_to_neuron_syn_lr.w": 15,
+    "CaDynamics_E2.gamma": 16,
+    "CaDynamics_E2.decay": 17,
+    "CaDynamics_E2.depth": 18,
+    "CaDynamics_E2.minCai": 19,
+    "Ca_HVA.gbar": 20,
+    "Ca_LVAst.gCa_LVAstbar": 21,
+    "Im.gImbar": 22,
+    "K_Pst.gK_Pstbar": 23,
+    "K_Tst.gK_Tstbar": 24,
+    "NaTg.gNaTgbar": 25,
+    "Nap_Et2.gNap_Et2bar": 26,
+    "SK_E2.gSK_E2bar": 27,
+    "SKv3_1.gSKv3_1bar": 28,
 }
-HX_P_COUNT = 16
+HX_P_COUNT = 29
+HX_LIB_NTYPE = 13
+
+
+class LibTable(C.Structure):
+    _fields_ = [("n", C.c_int), ("node", _ip), ("par", _dp)]
+
+
+class LibDesc(C.Structure):
+    _fields_ = [("t", LibTable * HX_LIB_NTYPE)]
 
 
 class GroupDesc(C.Structure):
@@ -78,6 +100,7 @@ class GroupDesc(C.Structure):
         ("nhalfgap", C.c_int), ("hg_node", _ip), ("hg_src", _ip), ("hg_g", _dp),
         ("ngapj", C.c_int), ("gj_node", _ip), ("gj_pre", _ip), ("gj_g", _dp), ("gj_w", _dp),
         ("ngraded", C.c_int), ("gr_node", _ip), ("gr_pre", _ip), ("gr_w", _dp), ("gr_delta", _dp), ("gr_vth", _dp),
+        ("lib", C.POINTER(LibDesc)),
     ]
 
 
@@ -242,6 +265,18 @@ class BoundGroup:
         gr = g.graded
         s.ngraded, s.gr_node, s.gr_pre = gr.n, I(gr.nodes), I(gr.ifields["pre"])
         s.gr_w, s.gr_delta, s.gr_vth = D(gr.fields["w"]), D(gr.fields["delta"]), D(gr.fields["Vth"])
+        self.lib = None
+        if any(t.n for t in g.lib.values()):
+            from .model import LIB_NAMES, lib_par_matrix
+
+            lb = LibDesc()
+            for t, nm in enumerate(LIB_NAMES):
+                tab = g.lib.get(nm)
+                lb.t[t].n = tab.n if tab is not None else 0
+                lb.t[t].node = I(tab.nodes if tab is not None else np.zeros(0, np.int32))
+                lb.t[t].par = D(lib_par_matrix(g, nm).reshape(-1))
+            self.lib = lb
+            s.lib = C.pointer(lb)
         self.desc = s
 
 

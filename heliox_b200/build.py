@@ -17,7 +17,7 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 ROOT = os.path.dirname(HERE)
 CSRC = os.path.join(HERE, "csrc")
 LIB = os.path.join(HERE, "libhx_b200.so")
-SOURCES = ["hx_kernels.cu", "hx_split.cu", "hx_runtime.cu", "hx_runtime_net.cu", "hx_netstim.cpp", "hx_plan.cpp", "hx_noalloc.cu"]
+SOURCES = ["hx_kernels.cu", "hx_split.cu", "hx_runtime.cu", "hx_runtime_net.cu", "hx_runtime_lib.cu", "hx_netstim.cpp", "hx_plan.cpp", "hx_noalloc.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 

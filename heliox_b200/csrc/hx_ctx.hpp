@@ -153,6 +153,14 @@ struct hx_ctx {
     int nranks = 1;
     size_t ck_net_stride = 0;  // doubles per checkpoint beyond v, m, h, n
 
+    // ---- library mechanisms (hx_lib.cuh; hx_runtime_lib.cu)
+    bool lib = false;
+    int lib_n[HX_LIB_NTYPE] = {0};  // instances per type
+    int lib_nst = 0;                // states over all entries
+    hx::DevLib L{};
+    DevBuf<int> lib_node_off, lib_ent, lib_ent_st, lib_ent_fix;
+    DevBuf<double> lib_fix, lib_st, lib_lam, lib_nica, lib_nlica, lib_tape, lib_ck;
+
     // ---- a cell split across CTAs (hx_split.cu)
     bool split = false;
     hx::DevSplit X{};
@@ -169,6 +177,10 @@ hx::DevProbe hx_probe_view(hx_ctx* c);
 int hx_setup_time(hx_ctx* ctx, int nstep);
 double* hx_kind_ptr(hx_ctx* c, int kind);
 size_t hx_grad_base(const hx_ctx* c, int kind);
+// library mechanisms (hx_runtime_lib.cu): entry tables, kinds 16.. maps and
+// device arrays; the type of a library parameter kind
+int hx_lib_load(hx_ctx* ctx, const hx_group_desc* desc);
+int hx_lib_type_of_kind(int kind);
 // network parts (hx_runtime_net.cu)
 int hx_net_load(hx_ctx* ctx, const hx_group_desc* desc);
 int hx_net_forward(hx_ctx* ctx, int nstep, double v_init, double* trace_dev, bool capture);

@@ -126,4 +126,30 @@ struct DevNet {
     const int *node_in_off, *node_in;  // incoming (kind << 28 | instance) per node
 };
 
+// Library mechanisms of a group (step kernels instantiated with kLib = true).
+// Entries are the mechanism instances in GPU node order, on one node in
+// CoreNEURON type order (ions, CaDynamics_E2, channels): entry e has code
+// type << 24 | instance (GPU instance order of its type), its states at
+// ent_st[e] of the flat state array (ca_ion: cai; channels: their gates) and
+// its fixed parameters at ent_fix[e] of fix (ions: erev / concentrations;
+// NaTg: vshifth, vshiftm, slopeh, slopem; SK_E2: zTau).  Trainable
+// parameters (HX_P_CADYN_GAMMA .. HX_P_SKV3_1_G) live per instance in
+// prm[kind - HX_P_CADYN_GAMMA], their gradients in grad[...].
+constexpr int kLibKinds = 13;
+struct DevLib {
+    int nst;
+    const int *node_off, *ent, *ent_st, *ent_fix;  // node_off: nnode + 1; ent_st: nent + 1
+    const double* fix;
+    const double* prm[kLibKinds];
+    double* grad[kLibKinds];
+    double* st;     // states at the current step
+    double* lam;    // adjoints of the states (backward)
+    double* nica;   // per node: calcium current of the forward's current step
+    double* nlica;  // per node: adjoint of the step's calcium current (backward)
+    double* tape;   // rows x nst: states at the start of each step, row 0 = step k_base
+    int k_base;
+    double ktf;  // 1000 R (celsius + 273.15) / F (eion.cuh:38-41)
+    double dt;
+};
+
 }  // namespace hx

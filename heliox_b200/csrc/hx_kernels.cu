@@ -45,6 +45,12 @@ __global__ void init_state_kernel(DevGroup G, DevState S, double v_init) {
     S.n[i] = n;
 }
 
+// finitialize of the library mechanisms (after init_state_kernel)
+__global__ void lib_init_kernel(DevLib L, int nnode, double v_init) {
+    const int gi = blockIdx.x * blockDim.x + threadIdx.x;
+    if (gi < nnode) lib::lib_init(L, gi, v_init);
+}
+
 // ------------------------------------------------------------------ forward
 // kNet adds, per step: PreSyn threshold detection at the step's start
 // (PreSyn::threshold_detect_cpu, presyn.cpp:133-177: a spike at t_k when
@@ -55,10 +61,15 @@ __global__ void init_state_kernel(DevGroup G, DevState S, double v_init) {
 // graded-synapse state updates.  In a coupled launch (gaps, graded
 // synapses; one step) partner voltages come from N.vpeer and v_{k+1} goes to
 // N.vout, so that no CTA reads a value another CTA rewrites.
-template <bool kNet>
+//
+// kLib adds the library mechanisms (hx_lib.cuh): their currents after the
+// other mechanisms in phase A, their state updates in phase C, and their
+// states in the tape (the cell's contiguous state range, row per step).
+template <bool kNet, bool kLib = false>
 __global__ void __launch_bounds__(kThreads, 1) fwd_kernel(DevGroup G, DevState S, DevTape T, int write_tape,
                                                            DevProbe P, double* __restrict__ trace,
-                                                           const double* __restrict__ tmid, int k0, int k1, DevNet N) {
+                                                           const double* __restrict__ tmid, int k0, int k1, DevNet N,
+                                                           DevLib L) {
     extern __shared__ double smem[];
     const int p = blockIdx.x;
     const int N_ = G.smem_n;
@@ -102,6 +113,11 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_kernel(DevGroup G, DevState S
         }
     }
     const int q0 = P.slot_off[g.slot], q1 = P.slot_off[g.slot + 1];
+    int ls0 = 0, ls1 = 0;  // kLib: the cell's range of the flat state array
+    if (kLib) {
+        ls0 = L.ent_st[L.node_off[pb + i0]];
+        ls1 = L.ent_st[L.node_off[pb + i1]];
+    }
     g.sync();
     if (k0 == 0 && trace)
         for (int q = q0 + g.tl; q < q1; q += g.nt) trace[P.slot[q]] = sv[P.local[q]];
@@ -111,6 +127,10 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_kernel(DevGroup G, DevState S
         const size_t toff = (size_t)(k - T.k_base) * (size_t)G.nnode + pb;
         if (write_tape)
             for (int i = i0 + g.tl; i < i1; i += g.nt) __stcs(T.v + toff + i, sv[i]);
+        if (kLib && write_tape) {
+            double* row = L.tape + (size_t)(k - L.k_base) * (size_t)L.nst;
+            for (int j = ls0 + g.tl; j < ls1; j += g.nt) __stcs(row + j, L.st[j]);
+        }
         if (kNet) {
             if (N.detect && g.tl == 0 && psnode >= 0) {
                 const double pv = sv[psnode];
@@ -192,6 +212,11 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_kernel(DevGroup G, DevState S
                 }
                 assemble<true, true>(G, M, pb, i, fl, q, vi, sv, sa, sb, gm, gh, gn, tm, r, dd, N, ssA, ssB, ps0,
                                      N.gr_s, N.vpeer);
+            } else if (kLib) {
+                double ica;
+                assemble<true, false, false, true>(G, M, pb, i, fl, q, vi, sv, sa, sb, gm, gh, gn, tm, r, dd, N,
+                                                   nullptr, nullptr, 0, nullptr, nullptr, &L, L.st, &ica);
+                L.nica[pb + i] = ica;
             } else {
                 assemble<true>(G, M, pb, i, fl, q, vi, sv, sa, sb, gm, gh, gn, tm, r, dd);
             }
@@ -207,6 +232,7 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_kernel(DevGroup G, DevState S
         // C: v update (the gates follow in the next step's A, or below)
         for (int i = i0 + g.tl; i < i1; i += g.nt) {
             sv[i] = sv[i] + srhs[i];
+            if (kLib) lib::lib_state(L, pb + i, sv[i], L.st);
             if (kNet) {  // synapse decay x + c (0 - x) (expsyn.cpp:125-134, exp2syn_temp.cuh:51-58)
                 const int s1 = __ldg(N.node_syn_off + pb + i + 1);
                 for (int j = __ldg(N.node_syn_off + pb + i); j < s1; ++j) {
@@ -223,6 +249,10 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_kernel(DevGroup G, DevState S
     if (write_tape) {
         const size_t off = (size_t)(k1 - T.k_base) * (size_t)G.nnode + pb;
         for (int i = i0 + g.tl; i < i1; i += g.nt) __stcs(T.v + off + i, sv[i]);
+        if (kLib) {
+            double* row = L.tape + (size_t)(k1 - L.k_base) * (size_t)L.nst;
+            for (int j = ls0 + g.tl; j < ls1; j += g.nt) __stcs(row + j, L.st[j]);
+        }
     }
     double* vdst = (kNet && N.coupled) ? N.vout : S.v;
     for (int i = i0 + g.tl; i < i1; i += g.nt) {
@@ -260,11 +290,14 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_kernel(DevGroup G, DevState S
 // Coupled launches (one step): the dL/dv_k contributions of a gap or graded
 // synapse to its partner node go through N.x_*_out and are gathered by the
 // launch of step k-1 from N.x_*_in, in the fixed order of N.node_in.
-template <bool kNet>
+// kLib: the library mechanisms' state-update adjoints join mu in S + A (their
+// currents recomputed from the tape give d_k and the calcium current), the
+// adjoints of their currents join dL/dv_k in V (hx_lib.cuh).
+template <bool kNet, bool kLib = false>
 __global__ void __launch_bounds__(kThreads, 1) bwd_kernel(DevGroup G, DevTape T, DevAdj Ad, DevGrad GR, DevProbe P,
                                                            const double* __restrict__ dLdv,
                                                            const double* __restrict__ tmid, int k_hi, int k_lo,
-                                                           DevNet N) {
+                                                           DevNet N, DevLib L) {
     extern __shared__ double smem[];
     const int p = blockIdx.x;
     const int N_ = G.smem_n;
@@ -353,6 +386,12 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_kernel(DevGroup G, DevTape T,
                 }
                 assemble<false, true>(G, M, pb, i, fl, q, vk, nullptr, sa, sb, gm, gh, gn, tm, r, dd, N, tA, tB, 0,
                                       grs, vpeer);
+            } else if (kLib) {
+                const double* Xk = L.tape + (size_t)(k - L.k_base) * (size_t)L.nst;
+                double ica;
+                assemble<false, false, false, true>(G, M, pb, i, fl, q, vk, nullptr, sa, sb, gm, gh, gn, tm, r, dd,
+                                                    N, nullptr, nullptr, 0, nullptr, nullptr, &L, Xk, &ica);
+                mu += lib::lib_state_adj(L, pb + i, T.v[off + G.nnode + i], Xk, Xk + L.nst, ica);
             } else {
                 assemble<false>(G, M, pb, i, fl, q, vk, nullptr, sa, sb, gm, gh, gn, tm, r, dd);
             }
@@ -389,6 +428,7 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_kernel(DevGroup G, DevTape T,
                 ln = lnv[i];
             }
             double lvn = vjp_mech(G, GR, T, off, i, gi, fl, q, w, vk, ld, tm, lvn0, lm, lh, ln);
+            if (kLib) lvn += lib::lib_current_adj(L, gi, vk, L.tape + (size_t)(k - L.k_base) * (size_t)L.nst, w, ld);
             if (fl & kHasHH) {
                 lmv[i] = lm;
                 lhv[i] = lh;
@@ -621,6 +661,10 @@ cudaError_t configure_kernels(size_t smem_fwd, size_t smem_bwd, size_t smem_fwd_
     if (e != cudaSuccess) return e;
     e = cudaFuncSetAttribute(bwd_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_bwd);
     if (e != cudaSuccess) return e;
+    e = cudaFuncSetAttribute(fwd_kernel<false, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_fwd);
+    if (e != cudaSuccess) return e;
+    e = cudaFuncSetAttribute(bwd_kernel<false, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_bwd);
+    if (e != cudaSuccess) return e;
     e = cudaFuncSetAttribute(fwd_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_fwd_net);
     if (e != cudaSuccess) return e;
     return cudaFuncSetAttribute(bwd_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_bwd_net);
@@ -631,25 +675,45 @@ cudaError_t launch_init(const DevGroup& G, const DevState& S, double v_init, cud
     return cudaGetLastError();
 }
 
+cudaError_t launch_lib_init(const DevLib& L, int nnode, double v_init, cudaStream_t st) {
+    if (nnode <= 0) return cudaSuccess;
+    lib_init_kernel<<<(nnode + 255) / 256, 256, 0, st>>>(L, nnode, v_init);
+    return cudaGetLastError();
+}
+
 cudaError_t launch_fwd(const DevGroup& G, const DevState& S, const DevTape& T, int write_tape, const DevProbe& P,
-                       double* trace, const double* tmid, int k0, int k1, cudaStream_t st, const DevNet* N) {
-    if (N)
+                       double* trace, const double* tmid, int k0, int k1, cudaStream_t st, const DevNet* N,
+                       const DevLib* L) {
+    if (N) {
         fwd_kernel<true><<<G.npack, kThreads, fwd_smem_bytes(G, N->smem_syn), st>>>(G, S, T, write_tape, P, trace,
-                                                                                   tmid, k0, k1, *N);
-    else
+                                                                                   tmid, k0, k1, *N, DevLib{});
+    } else if (L) {
+        DevLib Lk = *L;
+        Lk.k_base = T.k_base;
+        fwd_kernel<false, true><<<G.npack, kThreads, fwd_smem_bytes(G, 0), st>>>(G, S, T, write_tape, P, trace,
+                                                                                tmid, k0, k1, DevNet{}, Lk);
+    } else {
         fwd_kernel<false><<<G.npack, kThreads, fwd_smem_bytes(G, 0), st>>>(G, S, T, write_tape, P, trace, tmid, k0,
-                                                                          k1, DevNet{});
+                                                                          k1, DevNet{}, DevLib{});
+    }
     return cudaGetLastError();
 }
 
 cudaError_t launch_bwd(const DevGroup& G, const DevTape& T, const DevAdj& A, const DevGrad& GR, const DevProbe& P,
-                       const double* dLdv, const double* tmid, int k_hi, int k_lo, cudaStream_t st, const DevNet* N) {
-    if (N)
+                       const double* dLdv, const double* tmid, int k_hi, int k_lo, cudaStream_t st, const DevNet* N,
+                       const DevLib* L) {
+    if (N) {
         bwd_kernel<true><<<G.npack, kThreads, bwd_smem_bytes(G, N->smem_syn), st>>>(G, T, A, GR, P, dLdv, tmid, k_hi,
-                                                                                   k_lo, *N);
-    else
+                                                                                   k_lo, *N, DevLib{});
+    } else if (L) {
+        DevLib Lk = *L;
+        Lk.k_base = T.k_base;
+        bwd_kernel<false, true><<<G.npack, kThreads, bwd_smem_bytes(G, 0), st>>>(G, T, A, GR, P, dLdv, tmid, k_hi,
+                                                                                k_lo, DevNet{}, Lk);
+    } else {
         bwd_kernel<false><<<G.npack, kThreads, bwd_smem_bytes(G, 0), st>>>(G, T, A, GR, P, dLdv, tmid, k_hi, k_lo,
-                                                                          DevNet{});
+                                                                          DevNet{}, DevLib{});
+    }
     return cudaGetLastError();
 }
 

@@ -13,12 +13,15 @@ size_t split_fwd_smem_bytes(const DevGroup& G);
 size_t split_bwd_smem_bytes(const DevGroup& G);
 cudaError_t configure_kernels(size_t smem_fwd, size_t smem_bwd, size_t smem_fwd_net, size_t smem_bwd_net);
 cudaError_t launch_init(const DevGroup& G, const DevState& S, double v_init, cudaStream_t st);
-// N == nullptr: the plain kernels; otherwise the network instantiation
+cudaError_t launch_lib_init(const DevLib& L, int nnode, double v_init, cudaStream_t st);
+// N and L null: the plain kernels; N: the network instantiation; L: the
+// library-mechanism instantiation (its tape rows are counted from T.k_base)
 cudaError_t launch_fwd(const DevGroup& G, const DevState& S, const DevTape& T, int write_tape, const DevProbe& P,
-                       double* trace, const double* tmid, int k0, int k1, cudaStream_t st, const DevNet* N = nullptr);
+                       double* trace, const double* tmid, int k0, int k1, cudaStream_t st, const DevNet* N = nullptr,
+                       const DevLib* L = nullptr);
 cudaError_t launch_bwd(const DevGroup& G, const DevTape& T, const DevAdj& A, const DevGrad& GR, const DevProbe& P,
                        const double* dLdv, const double* tmid, int k_hi, int k_lo, cudaStream_t st,
-                       const DevNet* N = nullptr);
+                       const DevNet* N = nullptr, const DevLib* L = nullptr);
 // split cell (hx_split.cu): cooperative launches over all packs
 cudaError_t configure_split(size_t smem_fwd, size_t smem_bwd);
 const void* split_fwd_kernel_ptr();

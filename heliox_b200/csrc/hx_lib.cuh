@@ -1,0 +1,819 @@
+// hx_lib.cuh -- library mechanisms for the fused step kernels: the ions and
+// the user-mech channel set, each written once as a template over its scalar
+// type.  With double it is the forward; with the forward-mode dual numbers
+// below it yields the exact partial derivatives the adjoint needs, so a
+// mechanism added in this form gets its vector-Jacobian products without
+// hand-derived code.
+//
+// Every formula keeps the operation order of the reference's mechanism
+// (src/mech/user-mech/<name>.cu, cited per mechanism) and goes through the
+// MechTemp contract (src/mech/mech_template.cuh:589-767): current
+// I(v + 0.001) and I(v), conductance (I1 - I0) / 0.001, rhs -= I0, d += g,
+// the ion current accumulated from the I(v) call; state updates at the new
+// voltage, mechanisms that write an ion in their state update (CaDynamics_E2)
+// first (nonvint_cpu, src/simulate.cpp:784-852).  Ions follow
+// src/mech/eion.cuh: erev read from the instance (iontype 0) or recomputed by
+// the Nernst equation from cai / cao at finitialize and at the start of every
+// current phase (iontype 040 | 0100).
+//
+// The kernels are compiled with --fmad=false, so the primal part of a dual
+// evaluation is bit-identical to the double evaluation of the same template.
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include "hx_dev.hpp"
+#include "hx_mech.cuh"
+
+namespace hx {
+namespace lib {
+
+#define HXD __host__ __device__ __forceinline__
+
+// ------------------------------------------------------------ dual numbers
+template <int N>
+struct Dual {
+    double v;
+    double d[N];
+    HXD Dual() {}
+    HXD Dual(double x) : v(x) {
+#pragma unroll
+        for (int i = 0; i < N; ++i) d[i] = 0.0;
+    }
+    HXD static Dual var(double x, int k) {
+        Dual r(x);
+        r.d[k] = 1.0;
+        return r;
+    }
+};
+
+HXD double val(double x) { return x; }
+template <int N>
+HXD double val(const Dual<N>& x) {
+    return x.v;
+}
+
+template <int N>
+HXD Dual<N> operator+(const Dual<N>& a, const Dual<N>& b) {
+    Dual<N> r;
+    r.v = a.v + b.v;
+#pragma unroll
+    for (int i = 0; i < N; ++i) r.d[i] = a.d[i] + b.d[i];
+    return r;
+}
+template <int N>
+HXD Dual<N> operator+(const Dual<N>& a, double b) {
+    Dual<N> r = a;
+    r.v = a.v + b;
+    return r;
+}
+template <int N>
+HXD Dual<N> operator+(double a, const Dual<N>& b) {
+    Dual<N> r = b;
+    r.v = a + b.v;
+    return r;
+}
+template <int N>
+HXD Dual<N> operator-(const Dual<N>& a) {
+    Dual<N> r;
+    r.v = -a.v;
+#pragma unroll
+    for (int i = 0; i < N; ++i) r.d[i] = -a.d[i];
+    return r;
+}
+template <int N>
+HXD Dual<N> operator-(const Dual<N>& a, const Dual<N>& b) {
+    Dual<N> r;
+    r.v = a.v - b.v;
+#pragma unroll
+    for (int i = 0; i < N; ++i) r.d[i] = a.d[i] - b.d[i];
+    return r;
+}
+template <int N>
+HXD Dual<N> operator-(const Dual<N>& a, double b) {
+    Dual<N> r = a;
+    r.v = a.v - b;
+    return r;
+}
+template <int N>
+HXD Dual<N> operator-(double a, const Dual<N>& b) {
+    Dual<N> r;
+    r.v = a - b.v;
+#pragma unroll
+    for (int i = 0; i < N; ++i) r.d[i] = -b.d[i];
+    return r;
+}
+template <int N>
+HXD Dual<N> operator*(const Dual<N>& a, const Dual<N>& b) {
+    Dual<N> r;
+    r.v = a.v * b.v;
+#pragma unroll
+    for (int i = 0; i < N; ++i) r.d[i] = a.d[i] * b.v + a.v * b.d[i];
+    return r;
+}
+template <int N>
+HXD Dual<N> operator*(const Dual<N>& a, double b) {
+    Dual<N> r;
+    r.v = a.v * b;
+#pragma unroll
+    for (int i = 0; i < N; ++i) r.d[i] = a.d[i] * b;
+    return r;
+}
+template <int N>
+HXD Dual<N> operator*(double a, const Dual<N>& b) {
+    Dual<N> r;
+    r.v = a * b.v;
+#pragma unroll
+    for (int i = 0; i < N; ++i) r.d[i] = a * b.d[i];
+    return r;
+}
+template <int N>
+HXD Dual<N> operator/(const Dual<N>& a, const Dual<N>& b) {
+    Dual<N> r;
+    r.v = a.v / b.v;
+    const double ib = 1.0 / b.v;
+#pragma unroll
+    for (int i = 0; i < N; ++i) r.d[i] = (a.d[i] - r.v * b.d[i]) * ib;
+    return r;
+}
+template <int N>
+HXD Dual<N> operator/(const Dual<N>& a, double b) {
+    Dual<N> r;
+    r.v = a.v / b;
+#pragma unroll
+    for (int i = 0; i < N; ++i) r.d[i] = a.d[i] / b;
+    return r;
+}
+template <int N>
+HXD Dual<N> operator/(double a, const Dual<N>& b) {
+    Dual<N> r;
+    r.v = a / b.v;
+    const double s = -r.v / b.v;
+#pragma unroll
+    for (int i = 0; i < N; ++i) r.d[i] = s * b.d[i];
+    return r;
+}
+template <int N>
+HXD Dual<N> exp(const Dual<N>& a) {
+    Dual<N> r;
+    r.v = ::exp(a.v);
+#pragma unroll
+    for (int i = 0; i < N; ++i) r.d[i] = r.v * a.d[i];
+    return r;
+}
+template <int N>
+HXD Dual<N> log(const Dual<N>& a) {
+    Dual<N> r;
+    r.v = ::log(a.v);
+    const double ia = 1.0 / a.v;
+#pragma unroll
+    for (int i = 0; i < N; ++i) r.d[i] = a.d[i] * ia;
+    return r;
+}
+template <int N>
+HXD Dual<N> pow(const Dual<N>& a, double c) {
+    Dual<N> r;
+    r.v = ::pow(a.v, c);
+    const double s = c * ::pow(a.v, c - 1.0);
+#pragma unroll
+    for (int i = 0; i < N; ++i) r.d[i] = s * a.d[i];
+    return r;
+}
+HXD double exp(double x) { return ::exp(x); }
+HXD double log(double x) { return ::log(x); }
+HXD double pow(double x, double c) { return ::pow(x, c); }
+
+// ------------------------------------------------------------ shared forms
+// cnexp update of NaTg, Nap_Et2, SKv3_1, SK_E2, Im, K_Pst, K_Tst, Ca_LVAst:
+// x + (1 - exp(dt (-1/tau))) (-(inf/tau) / (-1/tau) - x)
+template <class T, class U>
+HXD T cnexp(const T& x, const T& inf, const U& tau, double dt) {
+    return x + (1.0 - exp(dt * (-1.0 / tau))) * (-(inf / tau) / (-1.0 / tau) - x);
+}
+
+HXD double qt23() { return ::pow(2.3, ((34.0 - 21.0) / 10.0)); }
+
+// Nernst potential of a divalent ion (eion.cuh:38-56 with z = 2)
+template <class T>
+HXD T nernst2(const T& ci, double co, double ktf) {
+    if (val(ci) <= 0.) return T(1e6);
+    if (co <= 0.) return T(-1e6);
+    return ktf / 2.0 * log(co / ci);
+}
+
+// ------------------------------------------------------------ channels
+// Each channel: kS states, kP trainable parameters (the density gbar), the
+// ion it reads erev of and writes its current to (0 Na, 1 K, 2 Ca), kCai when
+// its state update reads cai.  cur(v, s, p, f, e) is the value
+// current_single_node returns; state(v, dt, s, f, cai) the state update;
+// init the INITIAL block.
+
+// NaTg.cu:78-160
+struct NaTg {
+    static constexpr int kS = 2, kP = 1, kIon = 0;
+    static constexpr bool kCai = false;
+    template <class T>
+    HXD static void rates(const T& v, const double* f, T r[4]) {
+        const double qt = qt23();
+        const double vshifth = f[0], vshiftm = f[1], slopeh = f[2], slopem = f[3];
+        T v_m = v;
+        if (val(v_m) == -38.0) v_m = v_m + 0.0001;
+        const T mA = (0.182 * (v_m - (-38.0 + vshiftm))) / (1.0 - exp(-(v_m - (-38.0 + vshiftm)) / slopem));
+        const T mB = (0.124 * (-v_m + (-38.0 + vshiftm))) / (1.0 - exp(-(-v_m + (-38.0 + vshiftm)) / slopem));
+        r[1] = (1.0 / (mA + mB)) / qt;
+        r[0] = mA / (mA + mB);
+        T v_h = v;
+        if (val(v_h) == -66.0) v_h = v_h + 0.0001;
+        const T hA = (-0.015 * (v_h - (-66.0 + vshifth))) / (1.0 - exp((v_h - (-66.0 + vshifth)) / slopeh));
+        const T hB = (-0.015 * (-v_h + (-66.0 + vshifth))) / (1.0 - exp((-v_h + (-66.0 + vshifth)) / slopeh));
+        r[3] = (1.0 / (hA + hB)) / qt;
+        r[2] = hA / (hA + hB);
+    }
+    template <class T>
+    HXD static T cur(const T& v, const T* s, const T* p, const double*, const T& e) {
+        return p[0] * s[0] * s[0] * s[0] * s[1] * (v - e);
+    }
+    template <class T>
+    HXD static void state(const T& v, double dt, T* s, const double* f, const T&) {
+        T r[4];
+        rates(v, f, r);
+        s[0] = cnexp(s[0], r[0], r[1], dt);
+        s[1] = cnexp(s[1], r[2], r[3], dt);
+    }
+    HXD static void init(double v, double* s, const double* f, double) {
+        double r[4];
+        rates(v, f, r);
+        s[0] = r[0];
+        s[1] = r[2];
+    }
+};
+
+// Nap_Et2.cu
+struct NapEt2 {
+    static constexpr int kS = 2, kP = 1, kIon = 0;
+    static constexpr bool kCai = false;
+    template <class T>
+    HXD static void rates(const T& v, T r[4]) {
+        const double qt = qt23();
+        r[0] = 1.0 / (1.0 + exp((v - (-52.6)) / (-4.6)));
+        T v_m = v;
+        if (val(v_m) == -38.0) v_m = v_m + 0.0001;
+        const T mA = (0.182 * (v_m - (-38.0))) / (1.0 - exp(-(v_m - (-38.0)) / 6.0));
+        const T mB = (0.124 * (-v_m - 38.0)) / (1.0 - exp(-(-v_m - 38.0) / 6.0));
+        r[1] = 6.0 * (1.0 / (mA + mB)) / qt;
+        T v_h1 = v;
+        if (val(v_h1) == -17.0) v_h1 = v_h1 + 0.0001;
+        T v_h2 = v;
+        if (val(v_h2) == -64.4) v_h2 = v_h2 + 0.0001;
+        r[2] = 1.0 / (1.0 + exp((v - (-48.8)) / 10.0));
+        const T hA = -2.88e-6 * (v_h1 + 17.0) / (1.0 - exp((v_h1 + 17.0) / 4.63));
+        const T hB = 6.94e-6 * (v_h2 + 64.4) / (1.0 - exp(-(v_h2 + 64.4) / 2.63));
+        r[3] = (1.0 / (hA + hB)) / qt;
+    }
+    template <class T>
+    HXD static T cur(const T& v, const T* s, const T* p, const double*, const T& e) {
+        return p[0] * s[0] * s[0] * s[0] * s[1] * (v - e);
+    }
+    template <class T>
+    HXD static void state(const T& v, double dt, T* s, const double*, const T&) {
+        T r[4];
+        rates(v, r);
+        s[0] = cnexp(s[0], r[0], r[1], dt);
+        s[1] = cnexp(s[1], r[2], r[3], dt);
+    }
+    HXD static void init(double v, double* s, const double*, double) {
+        double r[4];
+        rates(v, r);
+        s[0] = r[0];
+        s[1] = r[2];
+    }
+};
+
+// K_Pst.cu
+struct KPst {
+    static constexpr int kS = 2, kP = 1, kIon = 1;
+    static constexpr bool kCai = false;
+    template <class T>
+    HXD static void rates(const T& v_param, T r[4]) {
+        const double qt = qt23();
+        const T v = v_param + 10.0;
+        r[0] = (1.0 / (1.0 + exp(-(v + 1.0) / 12.0)));
+        if (val(v) < -50.0)
+            r[1] = (1.25 + 175.03 * exp(-v * (-0.026))) / qt;
+        else
+            r[1] = ((1.25 + 13.0 * exp(-v * 0.026))) / qt;
+        r[2] = 1.0 / (1.0 + exp(-(v + 54.0) / (-11.0)));
+        r[3] = (360.0 + (1010.0 + 24.0 * (v + 55.0)) * exp(-pow(((v + 75.0) / 48.0), 2.0))) / qt;
+    }
+    template <class T>
+    HXD static T cur(const T& v, const T* s, const T* p, const double*, const T& e) {
+        return p[0] * s[0] * s[0] * s[1] * (v - e);
+    }
+    template <class T>
+    HXD static void state(const T& v, double dt, T* s, const double*, const T&) {
+        T r[4];
+        rates(v, r);
+        s[0] = cnexp(s[0], r[0], r[1], dt);
+        s[1] = cnexp(s[1], r[2], r[3], dt);
+    }
+    HXD static void init(double v, double* s, const double*, double) {
+        double r[4];
+        rates(v, r);
+        s[0] = r[0];
+        s[1] = r[2];
+    }
+};
+
+// K_Tst.cu
+struct KTst {
+    static constexpr int kS = 2, kP = 1, kIon = 1;
+    static constexpr bool kCai = false;
+    template <class T>
+    HXD static void rates(const T& v_param, T r[4]) {
+        const double qt = qt23();
+        const T v = v_param + 10.0;
+        r[0] = 1.0 / (1.0 + exp(-(v + 0.0) / 19.0));
+        r[1] = (0.34 + 0.92 * exp(-pow(((v + 71.0) / 59.0), 2.0))) / qt;
+        r[2] = 1.0 / (1.0 + exp(-(v + 66.0) / (-10.0)));
+        r[3] = (8.0 + 49.0 * exp(-pow(((v + 73.0) / 23.0), 2.0))) / qt;
+    }
+    template <class T>
+    HXD static T cur(const T& v, const T* s, const T* p, const double*, const T& e) {
+        return p[0] * pow(s[0], 4.0) * s[1] * (v - e);
+    }
+    template <class T>
+    HXD static void state(const T& v, double dt, T* s, const double*, const T&) {
+        T r[4];
+        rates(v, r);
+        s[0] = cnexp(s[0], r[0], r[1], dt);
+        s[1] = cnexp(s[1], r[2], r[3], dt);
+    }
+    HXD static void init(double v, double* s, const double*, double) {
+        double r[4];
+        rates(v, r);
+        s[0] = r[0];
+        s[1] = r[2];
+    }
+};
+
+// Ca_LVAst.cu
+struct CaLVAst {
+    static constexpr int kS = 2, kP = 1, kIon = 2;
+    static constexpr bool kCai = false;
+    template <class T>
+    HXD static void rates(const T& v_param, T r[4]) {
+        const double qt = qt23();
+        const T v = v_param + 10.0;
+        r[0] = 1.0 / (1.0 + exp((v - (-30.0)) / (-6.0)));
+        r[1] = (5.0 + 20.0 / (1.0 + exp((v - (-25.0)) / 5.0))) / qt;
+        r[2] = 1.0 / (1.0 + exp((v - (-80.0)) / 6.4));
+        r[3] = (20.0 + 50.0 / (1.0 + exp((v - (-40.0)) / 7.0))) / qt;
+    }
+    template <class T>
+    HXD static T cur(const T& v, const T* s, const T* p, const double*, const T& e) {
+        return p[0] * s[0] * s[0] * s[1] * (v - e);
+    }
+    template <class T>
+    HXD static void state(const T& v, double dt, T* s, const double*, const T&) {
+        T r[4];
+        rates(v, r);
+        s[0] = cnexp(s[0], r[0], r[1], dt);
+        s[1] = cnexp(s[1], r[2], r[3], dt);
+    }
+    HXD static void init(double v, double* s, const double*, double) {
+        double r[4];
+        rates(v, r);
+        s[0] = r[0];
+        s[1] = r[2];
+    }
+};
+
+// CA_HVA.cu (vtrap, rates, ca_hva_cal_current, state_single_node)
+struct CaHVA {
+    static constexpr int kS = 2, kP = 1, kIon = 2;
+    static constexpr bool kCai = false;
+    template <class T>
+    HXD static T vtrap(const T& x, double y) {
+        if (fabs(val(x) / y) < 1e-6) return y * (1.0 - x / y / 2.0);
+        return x / (exp(x / y) - 1.0);
+    }
+    template <class T>
+    HXD static void rates(const T& v, T r[4]) {
+        const T mA = 0.055 * vtrap(-27.0 - v, 3.8);
+        const T mB = 0.94 * exp((-75.0 - v) / 17.0);
+        r[0] = mA / (mA + mB);
+        r[1] = 1.0 / (mA + mB);
+        const T hA = 0.000457 * exp((-13.0 - v) / 50.0);
+        const T hB = 0.0065 / (exp((-v - 15.0) / 28.0) + 1.0);
+        r[2] = hA / (hA + hB);
+        r[3] = 1.0 / (hA + hB);
+    }
+    template <class T>
+    HXD static T cur(const T& v, const T* s, const T* p, const double*, const T& e) {
+        const T g = p[0] * s[0] * s[0] * s[1];
+        return g * (v - e);
+    }
+    template <class T>
+    HXD static void state(const T& v, double dt, T* s, const double*, const T&) {
+        T r[4];
+        rates(v, r);
+        s[0] = s[0] + (1.0 - exp(-dt / r[1])) * (r[0] - s[0]);
+        s[1] = s[1] + (1.0 - exp(-dt / r[3])) * (r[2] - s[1]);
+    }
+    HXD static void init(double v, double* s, const double*, double) {
+        double r[4];
+        rates(v, r);
+        s[0] = r[0];
+        s[1] = r[2];
+    }
+};
+
+// Im.cu
+struct Im {
+    static constexpr int kS = 1, kP = 1, kIon = 1;
+    static constexpr bool kCai = false;
+    template <class T>
+    HXD static void rates(const T& v, T r[2]) {
+        const double qt = qt23();
+        const T mA = 3.3e-3 * exp(2.5 * 0.04 * (v - (-35.0)));
+        const T mB = 3.3e-3 * exp(-2.5 * 0.04 * (v - (-35.0)));
+        r[0] = mA / (mA + mB);
+        r[1] = (1.0 / (mA + mB)) / qt;
+    }
+    template <class T>
+    HXD static T cur(const T& v, const T* s, const T* p, const double*, const T& e) {
+        return p[0] * s[0] * (v - e);
+    }
+    template <class T>
+    HXD static void state(const T& v, double dt, T* s, const double*, const T&) {
+        T r[2];
+        rates(v, r);
+        s[0] = cnexp(s[0], r[0], r[1], dt);
+    }
+    HXD static void init(double v, double* s, const double*, double) {
+        double r[2];
+        rates(v, r);
+        s[0] = r[0];
+    }
+};
+
+// SKv3_1.cu
+struct SKv31 {
+    static constexpr int kS = 1, kP = 1, kIon = 1;
+    static constexpr bool kCai = false;
+    template <class T>
+    HXD static void rates(const T& v, T r[2]) {
+        r[0] = 1.0 / (1.0 + exp((v - 18.700) / (-9.700)));
+        r[1] = 0.2 * 20.0 / (1.0 + exp((v - (-46.560)) / (-44.140)));
+    }
+    template <class T>
+    HXD static T cur(const T& v, const T* s, const T* p, const double*, const T& e) {
+        return p[0] * s[0] * (v - e);
+    }
+    template <class T>
+    HXD static void state(const T& v, double dt, T* s, const double*, const T&) {
+        T r[2];
+        rates(v, r);
+        s[0] = cnexp(s[0], r[0], r[1], dt);
+    }
+    HXD static void init(double v, double* s, const double*, double) {
+        double r[2];
+        rates(v, r);
+        s[0] = r[0];
+    }
+};
+
+// SK_E2.cu:70-132 (zTau: the mechanism's GLOBAL, f[0])
+struct SKE2 {
+    static constexpr int kS = 1, kP = 1, kIon = 1;
+    static constexpr bool kCai = true;
+    template <class T>
+    HXD static T zinf(const T& ca) {
+        T ca_safe = ca;
+        if (val(ca_safe) < 1e-7) ca_safe = ca_safe + 1e-07;
+        return 1.0 / (1.0 + pow((0.00043 / ca_safe), 4.8));
+    }
+    template <class T>
+    HXD static T cur(const T& v, const T* s, const T* p, const double*, const T& e) {
+        return p[0] * s[0] * (v - e);
+    }
+    template <class T>
+    HXD static void state(const T&, double dt, T* s, const double* f, const T& cai) {
+        s[0] = cnexp(s[0], zinf(cai), f[0], dt);
+    }
+    HXD static void init(double, double* s, const double*, double cai) { s[0] = zinf(cai); }
+};
+
+// CaDynamics_E2.cu:101-137: cai' from cai and the step's calcium current
+template <class T>
+HXD T cadyn(const T& cai, const T& ica, const T& gamma, const T& decay, const T& depth, const T& minCai, double dt) {
+    const double FARADAY = 96485.3321233100184;
+    const T drive_ica = -(10000.0) * (ica * gamma) / (2.0 * FARADAY * depth);
+    const T exp_factor = exp(dt * (-1.0 / decay));
+    const T steady_term = -(drive_ica - (-minCai) / decay) / (-1.0 / decay);
+    return cai + (1.0 - exp_factor) * (steady_term - cai);
+}
+
+// ------------------------------------------------------------ type table
+enum LibType : int {
+    kNaIon = 0, kKIon, kCaIon, kCaDyn, kCaHVA, kCaLVAst, kIm, kKPst, kKTst, kNaTg, kNapEt2, kSKE2, kSKv31, kNType
+};
+// first trainable kind of each type, relative to HX_P_CADYN_GAMMA (-1: none)
+__host__ __device__ constexpr int kind0(int t) {
+    return t < kCaDyn ? -1 : t == kCaDyn ? 0 : t + 0;
+}
+// states per entry / fixed parameters per entry / trainable parameters per instance
+__host__ __device__ constexpr int nstate(int t) {
+    return t == kCaIon ? 1 : (t == kIm || t == kSKE2 || t == kSKv31) ? 1 : t >= kCaHVA ? 2 : 0;
+}
+__host__ __device__ constexpr int nfix(int t) {
+    return (t == kNaIon || t == kKIon) ? 1 : t == kCaIon ? 4 : t == kNaTg ? 4 : t == kSKE2 ? 1 : 0;
+}
+__host__ __device__ constexpr int ntrain(int t) { return t < kCaDyn ? 0 : t == kCaDyn ? 4 : 1; }
+
+#define HX_LIB_CHANNELS(X) \
+    X(kCaHVA, CaHVA)       \
+    X(kCaLVAst, CaLVAst)   \
+    X(kIm, Im)             \
+    X(kKPst, KPst)         \
+    X(kKTst, KTst)         \
+    X(kNaTg, NaTg)         \
+    X(kNapEt2, NapEt2)     \
+    X(kSKE2, SKE2)         \
+    X(kSKv31, SKv31)
+
+// ------------------------------------------------------------ drivers
+// one channel's forward contribution; returns I(v) (the ion current)
+template <class M>
+__device__ __forceinline__ double fwd_cur(double v, const double* s, const double* p, const double* f, double e,
+                                          double& r, double& dd) {
+    double gg = M::template cur<double>(v + kFdEps, s, p, f, e);
+    const double i0 = M::template cur<double>(v, s, p, f, e);
+    gg = (gg - i0) / kFdEps;
+    r -= i0;
+    dd += gg;
+    return i0;
+}
+
+// Adjoint of one channel's part of step k: Phi = -w I(v) + ld (I(v+eps) -
+// I(v))/eps + li I(v) (w: adjoint of rhs, ld: of d, li: of the ion current).
+// Returns dPhi/dv, adds dPhi/ds to ls, dPhi/dp to gp and dPhi/de to le.
+template <class M>
+__device__ __forceinline__ double vjp_cur(double v, const double* s, const double* p, const double* f, double e,
+                                          double w, double ld, double li, double* ls, double* gp, double& le) {
+    constexpr int N = 2 + M::kS + M::kP;
+    using D = Dual<N>;
+    D ds[M::kS], dp[M::kP];
+#pragma unroll
+    for (int i = 0; i < M::kS; ++i) ds[i] = D::var(s[i], 1 + i);
+#pragma unroll
+    for (int i = 0; i < M::kP; ++i) dp[i] = D::var(p[i], 1 + M::kS + i);
+    const D dv = D::var(v, 0), de = D::var(e, N - 1);
+    const D i1 = M::template cur<D>(dv + kFdEps, ds, dp, f, de);
+    const D i0 = M::template cur<D>(dv, ds, dp, f, de);
+    double gr[N];
+#pragma unroll
+    for (int k = 0; k < N; ++k) gr[k] = (li - w) * i0.d[k] + ld * ((i1.d[k] - i0.d[k]) / kFdEps);
+#pragma unroll
+    for (int i = 0; i < M::kS; ++i) ls[i] += gr[1 + i];
+#pragma unroll
+    for (int i = 0; i < M::kP; ++i) gp[i] += gr[1 + M::kS + i];
+    le += gr[N - 1];
+    return gr[0];
+}
+
+// Adjoint of one channel's state update s_{k+1} = F(v_{k+1}, s_k[, cai_{k+1}]):
+// lam holds dL/ds_{k+1} on entry and dL/ds_k (through F) on return; returns
+// dL/dv_{k+1} through F and adds dL/dcai_{k+1} to lcai.
+template <class M>
+__device__ __forceinline__ double vjp_state(double v1, double dt, const double* s, const double* f, double cai,
+                                            double* lam, double& lcai) {
+    constexpr int N = 1 + M::kS + (M::kCai ? 1 : 0);
+    using D = Dual<N>;
+    D ds[M::kS];
+#pragma unroll
+    for (int i = 0; i < M::kS; ++i) ds[i] = D::var(s[i], 1 + i);
+    const D dv = D::var(v1, 0);
+    const D dc = M::kCai ? D::var(cai, N - 1) : D(cai);
+    M::template state<D>(dv, dt, ds, f, dc);
+    double acc[N];
+#pragma unroll
+    for (int k = 0; k < N; ++k) acc[k] = 0.0;
+#pragma unroll
+    for (int j = 0; j < M::kS; ++j) {
+        const double l = lam[j];
+#pragma unroll
+        for (int k = 0; k < N; ++k) acc[k] += l * ds[j].d[k];
+    }
+#pragma unroll
+    for (int i = 0; i < M::kS; ++i) lam[i] = acc[1 + i];
+    if (M::kCai) lcai += acc[N - 1];
+    return acc[0];
+}
+
+__device__ __forceinline__ int entry_type(int code) { return code >> 24; }
+__device__ __forceinline__ int entry_inst(int code) { return code & 0xFFFFFF; }
+
+// calcium reversal potential of a ca_ion entry (f: cai0, cao, eca, nernst)
+__device__ __forceinline__ double ca_erev(double cai, const double* f, double ktf) {
+    return f[3] != 0.0 ? nernst2(cai, f[1], ktf) : f[2];
+}
+
+// Current phase of GPU node gi at voltage v with the states X (the flat
+// state array of the step): adds the channels' rhs / d contributions in type
+// order and returns the node's calcium current.
+__device__ __forceinline__ double lib_current(const DevLib& L, int gi, double v, const double* X, double& r,
+                                              double& dd) {
+    const int e0 = __ldg(L.node_off + gi), e1 = __ldg(L.node_off + gi + 1);
+    double ena = 0.0, ek = 0.0, eca = 0.0, ica = 0.0;
+    for (int e = e0; e < e1; ++e) {
+        const int code = __ldg(L.ent + e), t = entry_type(code), inst = entry_inst(code);
+        const double* s = X + __ldg(L.ent_st + e);
+        const double* f = L.fix + __ldg(L.ent_fix + e);
+        switch (t) {
+            case kNaIon:
+                ena = __ldg(f);
+                break;
+            case kKIon:
+                ek = __ldg(f);
+                break;
+            case kCaIon:
+                eca = ca_erev(s[0], f, L.ktf);
+                break;
+#define HX_LIB_FWD(T_, M_)                                                          \
+    case T_: {                                                                      \
+        const double p[1] = {__ldg(L.prm[kind0(T_)] + inst)};                       \
+        const double e_ = M_::kIon == 0 ? ena : M_::kIon == 1 ? ek : eca;           \
+        const double i0 = fwd_cur<M_>(v, s, p, f, e_, r, dd);                       \
+        if (M_::kIon == 2) ica += i0;                                               \
+    } break;
+                HX_LIB_CHANNELS(HX_LIB_FWD)
+#undef HX_LIB_FWD
+            default:
+                break;
+        }
+    }
+    return ica;
+}
+
+// State phase of GPU node gi at the new voltage v: CaDynamics_E2 (from the
+// step's calcium current nica) before the channels, then the channels in type
+// order, updating X in place.
+__device__ __forceinline__ void lib_state(const DevLib& L, int gi, double v, double* X) {
+    const int e0 = __ldg(L.node_off + gi), e1 = __ldg(L.node_off + gi + 1);
+    int cs = -1;
+    for (int e = e0; e < e1; ++e) {
+        const int code = __ldg(L.ent + e), t = entry_type(code), inst = entry_inst(code);
+        double* s = X + __ldg(L.ent_st + e);
+        const double* f = L.fix + __ldg(L.ent_fix + e);
+        switch (t) {
+            case kCaIon:
+                cs = __ldg(L.ent_st + e);
+                break;
+            case kCaDyn:
+                X[cs] = cadyn<double>(X[cs], L.nica[gi], __ldg(L.prm[0] + inst), __ldg(L.prm[1] + inst),
+                                      __ldg(L.prm[2] + inst), __ldg(L.prm[3] + inst), L.dt);
+                break;
+#define HX_LIB_ST(T_, M_)                                                    \
+    case T_:                                                                 \
+        M_::template state<double>(v, L.dt, s, f, cs >= 0 ? X[cs] : 0.0);   \
+        break;
+                HX_LIB_CHANNELS(HX_LIB_ST)
+#undef HX_LIB_ST
+            default:
+                break;
+        }
+    }
+}
+
+// finitialize of GPU node gi at v: ca_ion's initial cai, the channels' INITIAL
+// blocks in type order.
+__device__ __forceinline__ void lib_init(const DevLib& L, int gi, double v) {
+    const int e0 = L.node_off[gi], e1 = L.node_off[gi + 1];
+    double cai = 0.0;
+    for (int e = e0; e < e1; ++e) {
+        const int t = entry_type(L.ent[e]);
+        double* s = L.st + L.ent_st[e];
+        const double* f = L.fix + L.ent_fix[e];
+        switch (t) {
+            case kCaIon:
+                cai = f[0];
+                s[0] = cai;
+                break;
+#define HX_LIB_INIT(T_, M_)       \
+    case T_:                      \
+        M_::init(v, s, f, cai);   \
+        break;
+                HX_LIB_CHANNELS(HX_LIB_INIT)
+#undef HX_LIB_INIT
+            default:
+                break;
+        }
+    }
+}
+
+// Adjoint of the state phase of step k at GPU node gi: v1 = v_{k+1}, Xk / Xk1
+// the states at the start of steps k / k+1, ica the step's calcium current.
+// L.lam holds dL/dX_{k+1} on entry; on return the state-phase part of
+// dL/dX_k, and L.nlica[gi] the adjoint of ica.  Returns dL/dv_{k+1} through
+// the state updates.
+__device__ __forceinline__ double lib_state_adj(const DevLib& L, int gi, double v1, const double* Xk,
+                                                const double* Xk1, double ica) {
+    const int e0 = __ldg(L.node_off + gi), e1 = __ldg(L.node_off + gi + 1);
+    if (e0 == e1) return 0.0;
+    int cs = -1;
+    for (int e = e0; e < e1 && e < e0 + 3; ++e)
+        if (entry_type(__ldg(L.ent + e)) == kCaIon) cs = __ldg(L.ent_st + e);
+    const double cai1 = cs >= 0 ? Xk1[cs] : 0.0;
+    double* lam = L.lam;
+    double mu = 0.0, lcai1 = 0.0;
+    bool dyn = false;
+    for (int e = e1 - 1; e >= e0; --e) {
+        const int code = __ldg(L.ent + e), t = entry_type(code), inst = entry_inst(code);
+        const int so = __ldg(L.ent_st + e);
+        const double* f = L.fix + __ldg(L.ent_fix + e);
+        switch (t) {
+#define HX_LIB_SADJ(T_, M_)                                                 \
+    case T_:                                                                \
+        mu += vjp_state<M_>(v1, L.dt, Xk + so, f, cai1, lam + so, lcai1);  \
+        break;
+            HX_LIB_CHANNELS(HX_LIB_SADJ)
+#undef HX_LIB_SADJ
+            case kCaDyn: {
+                dyn = true;
+                using D = Dual<6>;
+                const double lt = lam[cs] + lcai1;
+                const D out = cadyn<D>(D::var(Xk[cs], 0), D::var(ica, 1), D::var(__ldg(L.prm[0] + inst), 2),
+                                       D::var(__ldg(L.prm[1] + inst), 3), D::var(__ldg(L.prm[2] + inst), 4),
+                                       D::var(__ldg(L.prm[3] + inst), 5), L.dt);
+                lam[cs] = lt * out.d[0];
+                L.nlica[gi] = lt * out.d[1];
+#pragma unroll
+                for (int j = 0; j < 4; ++j) L.grad[j][inst] += lt * out.d[2 + j];
+            } break;
+            case kCaIon:
+                if (!dyn) {  // no calcium dynamics: cai_{k+1} = cai_k
+                    lam[cs] += lcai1;
+                    L.nlica[gi] = 0.0;
+                }
+                break;
+            default:
+                break;
+        }
+    }
+    return mu;
+}
+
+// Adjoint of the current phase of step k at GPU node gi (v_k = v, states Xk)
+// with w = dL/drhs_k, ld = dL/dd_k: adds dL/dX_k to L.lam and the parameter
+// gradients; returns dL/dv_k through the library currents.
+__device__ __forceinline__ double lib_current_adj(const DevLib& L, int gi, double v, const double* Xk, double w,
+                                                  double ld) {
+    const int e0 = __ldg(L.node_off + gi), e1 = __ldg(L.node_off + gi + 1);
+    if (e0 == e1) return 0.0;
+    double* lam = L.lam;
+    double ena = 0.0, ek = 0.0, eca = 0.0, lica = 0.0, leca = 0.0, lv = 0.0;
+    int cs = -1;
+    const double* fca = nullptr;
+    for (int e = e0; e < e1; ++e) {
+        const int code = __ldg(L.ent + e), t = entry_type(code), inst = entry_inst(code);
+        const int so = __ldg(L.ent_st + e);
+        const double* f = L.fix + __ldg(L.ent_fix + e);
+        switch (t) {
+            case kNaIon:
+                ena = __ldg(f);
+                break;
+            case kKIon:
+                ek = __ldg(f);
+                break;
+            case kCaIon:
+                cs = so;
+                fca = f;
+                eca = ca_erev(Xk[so], f, L.ktf);
+                lica = L.nlica[gi];
+                break;
+#define HX_LIB_CADJ(T_, M_)                                                                    \
+    case T_: {                                                                                 \
+        const double p[1] = {__ldg(L.prm[kind0(T_)] + inst)};                                  \
+        const double e_ = M_::kIon == 0 ? ena : M_::kIon == 1 ? ek : eca;                      \
+        double gp[1] = {0.0}, le = 0.0;                                                        \
+        lv += vjp_cur<M_>(v, Xk + so, p, f, e_, w, ld, M_::kIon == 2 ? lica : 0.0, lam + so,   \
+                          gp, le);                                                             \
+        L.grad[kind0(T_)][inst] += gp[0];                                                      \
+        if (M_::kIon == 2) leca += le;                                                         \
+    } break;
+                HX_LIB_CHANNELS(HX_LIB_CADJ)
+#undef HX_LIB_CADJ
+            default:
+                break;
+        }
+    }
+    if (cs >= 0 && fca[3] != 0.0 && Xk[cs] > 0.0 && fca[1] > 0.0)  // eca = ktf/2 log(cao/cai)
+        lam[cs] += leca * (-(L.ktf / 2.0) / Xk[cs]);
+    return lv;
+}
+
+#undef HXD
+
+}  // namespace lib
+}  // namespace hx

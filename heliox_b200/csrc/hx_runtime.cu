@@ -61,6 +61,8 @@ static size_t kind_count(const hx_ctx* c, int kind) {
         case HX_P_GRADED_W:
             return (size_t)c->ngr;
     }
+    const int lt = hx_lib_type_of_kind(kind);
+    if (lt >= 0) return (size_t)c->lib_n[lt];
     return 0;
 }
 
@@ -85,6 +87,8 @@ static size_t kind_store(const hx_ctx* c, int kind) {
         case HX_P_GRADED_W:
             return (size_t)c->ngr;
     }
+    const int lt = hx_lib_type_of_kind(kind);
+    if (lt >= 0) return (size_t)c->lib_n[lt];  // per instance, GPU instance order
     return (size_t)c->P.nnode;
 }
 
@@ -371,6 +375,8 @@ int hx_load_group(hx_ctx* ctx, const hx_group_desc* desc) {
         }
         HXC(ctx->kmap[k].upload(m, st));
     }
+    // library mechanism tables (kinds HX_P_CADYN_GAMMA..)
+    if (hx_lib_load(ctx, desc)) return -1;
     // node-indexed copies of reference-ordered arrays
     auto node_arr = [&](const double* src) {
         std::vector<double> out(std::max<size_t>(nn, 1), 0.0);
@@ -410,6 +416,7 @@ int hx_load_group(hx_ctx* ctx, const hx_group_desc* desc) {
     ctx->grad_off[0] = 0;
     for (int k = 0; k < HX_P_COUNT; k++) ctx->grad_off[k + 1] = ctx->grad_off[k] + kind_store(ctx, k);
     HXC(ctx->grad.ensure(ctx->grad_off[HX_P_COUNT]));
+    for (int k = 0; k < hx::kLibKinds; k++) ctx->L.grad[k] = ctx->grad.p + ctx->grad_off[HX_P_CADYN_GAMMA + k];
     HXC(ctx->stage_dev.ensure(ctx->grad_off[HX_P_COUNT] + std::max(nn, (size_t)ctx->nsyn)));
 
     hx::DevGroup& G = ctx->G;
@@ -466,6 +473,7 @@ int hx_load_group(hx_ctx* ctx, const hx_group_desc* desc) {
     G.cfac = 0.001 * (1.0 / desc->dt);                  // capac.cpp:56,70 with cj = 1/dt
     G.q10 = std::pow(3.0, (desc->celsius - 6.3) / 10);  // hh_templated.cu:90
     ctx->split = P.nsub > 0;
+    if (ctx->split && ctx->lib) return fail(ctx, "library mechanisms on a cell split across CTAs are not supported");
     size_t sf = ctx->split ? hx::split_fwd_smem_bytes(G) : hx::fwd_smem_bytes(G);
     size_t sb = ctx->split ? hx::split_bwd_smem_bytes(G) : hx::bwd_smem_bytes(G);
     size_t sfn = hx::fwd_smem_bytes(G, ctx->N.smem_syn), sbn = hx::bwd_smem_bytes(G, ctx->N.smem_syn);
@@ -641,8 +649,8 @@ int hx_setup_time(hx_ctx* ctx, int nstep) {
 }
 
 static int plan_tape(hx_ctx* ctx, int nstep) {
-    const size_t nn = ctx->P.nnode;
-    const size_t per_step = 4 * nn * sizeof(double);  // v, m, h, n
+    const size_t nn = ctx->P.nnode, nls = (size_t)ctx->lib_nst;
+    const size_t per_step = (4 * nn + nls) * sizeof(double);  // v, m, h, n, library states
     size_t budget = ctx->tape_budget;
     if (!budget) {
         size_t fr = 0, tot = 0;
@@ -658,6 +666,7 @@ static int plan_tape(hx_ctx* ctx, int nstep) {
         HXC(ctx->tm.ensure(nn * (size_t)(nstep + 1)));
         HXC(ctx->th.ensure(nn * (size_t)(nstep + 1)));
         HXC(ctx->tn.ensure(nn * (size_t)(nstep + 1)));
+        if (ctx->lib) HXC(ctx->lib_tape.ensure(nls * (size_t)(nstep + 1)));
         return 0;
     }
     // checkpointed: segments of K steps; (K+1) tape rows + one checkpoint per segment within budget
@@ -674,6 +683,10 @@ static int plan_tape(hx_ctx* ctx, int nstep) {
     HXC(ctx->th.ensure(nn * (K + 1)));
     HXC(ctx->tn.ensure(nn * (K + 1)));
     HXC(ctx->ck.ensure(4 * nn * (size_t)ctx->nseg));
+    if (ctx->lib) {
+        HXC(ctx->lib_tape.ensure(nls * (K + 1)));
+        HXC(ctx->lib_ck.ensure(nls * (size_t)ctx->nseg));
+    }
     return 0;
 }
 
@@ -689,13 +702,26 @@ static int copy_ck(hx_ctx* ctx, int s, bool save) {
         else
             HXC(cudaMemcpyAsync(st[k], base + k * nn, nn * 8, cudaMemcpyDeviceToDevice, ctx->st));
     }
+    if (ctx->lib && ctx->lib_nst) {
+        const size_t nls = (size_t)ctx->lib_nst;
+        double* lb = ctx->lib_ck.p + nls * (size_t)s;
+        if (save)
+            HXC(cudaMemcpyAsync(lb, ctx->lib_st.p, nls * 8, cudaMemcpyDeviceToDevice, ctx->st));
+        else
+            HXC(cudaMemcpyAsync(ctx->lib_st.p, lb, nls * 8, cudaMemcpyDeviceToDevice, ctx->st));
+    }
     return 0;
 }
 
 // plain or split-cell kernels (the split ones reset their barrier state per launch)
 static cudaError_t fwd_launch(hx_ctx* ctx, const hx::DevState& S, const hx::DevTape& T, int write_tape,
                               const hx::DevProbe& PV, double* trace, int k0, int k1) {
-    if (!ctx->split) return hx::launch_fwd(ctx->G, S, T, write_tape, PV, trace, ctx->tmid.p, k0, k1, ctx->st);
+    if (!ctx->split) {
+        if (!ctx->lib) return hx::launch_fwd(ctx->G, S, T, write_tape, PV, trace, ctx->tmid.p, k0, k1, ctx->st);
+        hx::DevLib Lv = ctx->L;
+        Lv.tape = ctx->lib_tape.p;
+        return hx::launch_fwd(ctx->G, S, T, write_tape, PV, trace, ctx->tmid.p, k0, k1, ctx->st, nullptr, &Lv);
+    }
     cudaError_t e = cudaMemsetAsync(ctx->split_bar.p, 0, 2 * sizeof(unsigned), ctx->st);
     if (e != cudaSuccess) return e;
     return hx::launch_split_fwd(ctx->G, S, T, write_tape, PV, trace, ctx->tmid.p, k0, k1, ctx->X, ctx->st);
@@ -703,7 +729,12 @@ static cudaError_t fwd_launch(hx_ctx* ctx, const hx::DevState& S, const hx::DevT
 
 static cudaError_t bwd_launch(hx_ctx* ctx, const hx::DevTape& T, const hx::DevAdj& A, const hx::DevGrad& GR,
                               const hx::DevProbe& PV, const double* dLdv, int k_hi, int k_lo) {
-    if (!ctx->split) return hx::launch_bwd(ctx->G, T, A, GR, PV, dLdv, ctx->tmid.p, k_hi, k_lo, ctx->st);
+    if (!ctx->split) {
+        if (!ctx->lib) return hx::launch_bwd(ctx->G, T, A, GR, PV, dLdv, ctx->tmid.p, k_hi, k_lo, ctx->st);
+        hx::DevLib Lv = ctx->L;
+        Lv.tape = ctx->lib_tape.p;
+        return hx::launch_bwd(ctx->G, T, A, GR, PV, dLdv, ctx->tmid.p, k_hi, k_lo, ctx->st, nullptr, &Lv);
+    }
     cudaError_t e = cudaMemsetAsync(ctx->split_bar.p, 0, 2 * sizeof(unsigned), ctx->st);
     if (e != cudaSuccess) return e;
     return hx::launch_split_bwd(ctx->G, T, A, GR, PV, dLdv, ctx->tmid.p, k_hi, k_lo, ctx->X, ctx->st);
@@ -735,6 +766,7 @@ static int run_forward(hx_ctx* ctx, int nstep, double v_init, int nprobe, const 
     hx::DevState S = state_view(ctx);
     hx::DevProbe PV = hx_probe_view(ctx);
     HXC(hx::launch_init(ctx->G, S, v_init, ctx->st));
+    if (ctx->lib) HXC(hx::launch_lib_init(ctx->L, (int)ctx->P.nnode, v_init, ctx->st));
     if (ctx->split) HXC(cudaMemsetAsync(ctx->split_err.p, 0, 4, ctx->st));
     HXC(cudaEventRecord(ctx->ev[0], ctx->st));
     int launches = 0;
@@ -768,6 +800,7 @@ static int run_backward(hx_ctx* ctx, const double* dLdv_dev) {
     HXC(cudaMemsetAsync(ctx->lh.p, 0, nn * 8, ctx->st));
     HXC(cudaMemsetAsync(ctx->ln.p, 0, nn * 8, ctx->st));
     HXC(cudaMemsetAsync(ctx->grad.p, 0, ctx->grad_off[HX_P_COUNT] * 8, ctx->st));
+    if (ctx->lib && ctx->lib_nst) HXC(cudaMemsetAsync(ctx->lib_lam.p, 0, (size_t)ctx->lib_nst * 8, ctx->st));
     hx::DevAdj A{ctx->lv.p, ctx->lm.p, ctx->lh.p, ctx->ln.p};
     double* g = ctx->grad.p;
     hx::DevGrad GR{g + ctx->grad_off[HX_P_HH_GNABAR], g + ctx->grad_off[HX_P_HH_GKBAR], g + ctx->grad_off[HX_P_HH_GL],

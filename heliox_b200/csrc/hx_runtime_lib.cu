@@ -1,0 +1,188 @@
+// hx_runtime_lib.cu -- host side of the library mechanisms (hx_lib.cuh):
+// the per-node entry tables in GPU order, the parameter kinds
+// HX_P_CADYN_GAMMA .. HX_P_SKV3_1_G, and the device arrays of DevLib.
+//
+// The reference keeps one instance table per mechanism type
+// (MechTemp::reg_node_indices / read_data_from_coredat,
+// src/mech/mech_template.cuh:192-368) and reaches an instance's ion through
+// the node (var_struct.cuh:376-470).  Here the instances of all library types
+// on one node are one run of entries, in type order, so that the thread that
+// owns the node walks them in the order the reference's type loop applies
+// them.
+#include <cmath>
+#include <string>
+#include <vector>
+
+#include "hx_ctx.hpp"
+#include "hx_lib.cuh"
+
+namespace {
+
+int fail(hx_ctx* c, const std::string& m) { return hx_fail(c, m); }
+
+#define HXC(call)                                                                                    \
+    do {                                                                                             \
+        cudaError_t _e = (call);                                                                     \
+        if (_e != cudaSuccess) return fail(ctx, std::string(#call) + ": " + cudaGetErrorString(_e)); \
+    } while (0)
+
+const char* kTypeName[HX_LIB_NTYPE] = {"na_ion",  "k_ion",  "ca_ion",  "CaDynamics_E2", "Ca_HVA",
+                                       "Ca_LVAst", "Im",     "K_Pst",   "K_Tst",         "NaTg",
+                                       "Nap_Et2",  "SK_E2",  "SKv3_1"};
+
+// ions a type needs on its node: bit 0 Na, 1 K, 2 Ca
+int ions_needed(int t) {
+    switch (t) {
+        case HX_LIB_NATG:
+        case HX_LIB_NAP_ET2:
+            return 1;
+        case HX_LIB_IM:
+        case HX_LIB_K_PST:
+        case HX_LIB_K_TST:
+        case HX_LIB_SKV3_1:
+            return 2;
+        case HX_LIB_SK_E2:
+            return 2 | 4;
+        case HX_LIB_CADYN:
+        case HX_LIB_CA_HVA:
+        case HX_LIB_CA_LVAST:
+            return 4;
+    }
+    return 0;
+}
+
+}  // namespace
+
+int hx_lib_type_of_kind(int kind) {
+    if (kind >= HX_P_CADYN_GAMMA && kind <= HX_P_CADYN_MINCAI) return HX_LIB_CADYN;
+    if (kind >= HX_P_CA_HVA_G && kind <= HX_P_SKV3_1_G) return kind - HX_P_CA_HVA_G + HX_LIB_CA_HVA;
+    return -1;
+}
+
+int hx_lib_load(hx_ctx* ctx, const hx_group_desc* desc) {
+    namespace L = hx::lib;
+    ctx->lib = false;
+    ctx->lib_nst = 0;
+    ctx->L = hx::DevLib{};
+    for (int t = 0; t < HX_LIB_NTYPE; t++) ctx->lib_n[t] = 0;
+    const hx_lib_desc* D = desc->lib;
+    bool any = false;
+    if (D)
+        for (int t = 0; t < HX_LIB_NTYPE; t++) {
+            if (D->t[t].n < 0) return fail(ctx, std::string("negative count of library table ") + kTypeName[t]);
+            if (D->t[t].n > 0 && (!D->t[t].node || !D->t[t].par))
+                return fail(ctx, std::string("library table ") + kTypeName[t] + " needs node and par arrays");
+            if (D->t[t].n >= (1 << 24)) return fail(ctx, std::string("too many instances of ") + kTypeName[t]);
+            any = any || D->t[t].n > 0;
+        }
+    cudaStream_t st = ctx->st;
+    if (!any) {
+        for (int k = HX_P_CADYN_GAMMA; k <= HX_P_SKV3_1_G; k++) {
+            ctx->kmap_h[k].assign(1, 0);
+            HXC(ctx->kmap[k].upload(ctx->kmap_h[k], st));
+            HXC(ctx->prm[k].ensure(1));
+        }
+        return 0;
+    }
+    if (ctx->net) return fail(ctx, "library mechanisms cannot be combined with network parts");
+    const hx::Plan& P = ctx->P;
+    const int nn = P.nnode;
+    // reference node -> instance of each type
+    std::vector<std::vector<int>> at(HX_LIB_NTYPE, std::vector<int>(nn, -1));
+    for (int t = 0; t < HX_LIB_NTYPE; t++) {
+        const hx_lib_table& T = D->t[t];
+        for (int j = 0; j < T.n; j++) {
+            const int r = T.node[j];
+            if (r < 0 || r >= nn) return fail(ctx, std::string(kTypeName[t]) + ": node index out of range");
+            if (j > 0 && r <= T.node[j - 1])
+                return fail(ctx, std::string(kTypeName[t]) + ": nodes must be sorted, one instance per node");
+            at[t][r] = j;
+        }
+        ctx->lib_n[t] = T.n;
+    }
+    for (int t = HX_LIB_CADYN; t < HX_LIB_NTYPE; t++) {
+        const int need = ions_needed(t);
+        for (int j = 0; j < D->t[t].n; j++) {
+            const int r = D->t[t].node[j];
+            if (((need & 1) && at[HX_LIB_NA_ION][r] < 0) || ((need & 2) && at[HX_LIB_K_ION][r] < 0) ||
+                ((need & 4) && at[HX_LIB_CA_ION][r] < 0))
+                return fail(ctx, std::string(kTypeName[t]) + " on node " + std::to_string(r) +
+                                     " needs its ion (na_ion / k_ion / ca_ion) on that node");
+        }
+    }
+    for (int j = 0; j < D->t[HX_LIB_CA_ION].n; j++)
+        if (!(D->t[HX_LIB_CA_ION].par[4 * j] > 0.0)) return fail(ctx, "ca_ion: cai must be positive");
+    // entries in GPU node order, types ascending on a node
+    std::vector<int> node_off(nn + 1, 0), ent, ent_st, ent_fix;
+    std::vector<double> fix;
+    std::vector<int> inst(HX_LIB_NTYPE, 0);
+    std::vector<std::vector<double>> prm(hx::kLibKinds);
+    for (int k = 0; k < hx::kLibKinds; k++) prm[k].assign(1, 0.0);
+    for (int k = HX_P_CADYN_GAMMA; k <= HX_P_SKV3_1_G; k++)
+        ctx->kmap_h[k].assign(std::max(ctx->lib_n[hx_lib_type_of_kind(k)], 1), 0);
+    int nst = 0;
+    for (int gi = 0; gi < nn; gi++) {
+        const int r = P.gpu2ref[gi];
+        for (int t = 0; t < HX_LIB_NTYPE; t++) {
+            const int j = at[t][r];
+            if (j < 0) continue;
+            const int ntr = L::ntrain(t), nfx = L::nfix(t), q = inst[t]++;
+            const double* par = D->t[t].par + (size_t)(ntr + nfx) * j;
+            ent.push_back(t << 24 | q);
+            ent_st.push_back(nst);
+            nst += L::nstate(t);
+            ent_fix.push_back((int)fix.size());
+            for (int c = 0; c < nfx; c++) fix.push_back(par[ntr + c]);
+            const int k0 = L::kind0(t);
+            for (int c = 0; c < ntr; c++) {
+                std::vector<double>& pv = prm[k0 + c];
+                if ((int)pv.size() < ctx->lib_n[t]) pv.resize(ctx->lib_n[t], 0.0);
+                pv[q] = par[c];
+                ctx->kmap_h[HX_P_CADYN_GAMMA + k0 + c][j] = q;
+            }
+        }
+        node_off[gi + 1] = (int)ent.size();
+    }
+    ent_st.push_back(nst);
+    if (fix.empty()) fix.push_back(0.0);
+    if (ent.empty()) ent.push_back(0);
+    const double sk_tau = D->t[HX_LIB_SK_E2].n ? D->t[HX_LIB_SK_E2].par[1] : 0.0;
+    for (int j = 1; j < D->t[HX_LIB_SK_E2].n; j++)
+        if (D->t[HX_LIB_SK_E2].par[2 * j + 1] != sk_tau)
+            return fail(ctx, "SK_E2: zTau is a GLOBAL of the mechanism, one value for all instances");
+    HXC(ctx->lib_node_off.upload(node_off, st));
+    HXC(ctx->lib_ent.upload(ent, st));
+    HXC(ctx->lib_ent_st.upload(ent_st, st));
+    HXC(ctx->lib_ent_fix.upload(ent_fix, st));
+    HXC(ctx->lib_fix.upload(fix, st));
+    for (int k = HX_P_CADYN_GAMMA; k <= HX_P_SKV3_1_G; k++) {
+        HXC(ctx->kmap[k].upload(ctx->kmap_h[k], st));
+        HXC(ctx->prm[k].upload(prm[k - HX_P_CADYN_GAMMA], st));
+    }
+    HXC(ctx->lib_st.ensure(std::max(nst, 1)));
+    HXC(ctx->lib_lam.ensure(std::max(nst, 1)));
+    HXC(ctx->lib_nica.ensure(std::max(nn, 1)));
+    HXC(ctx->lib_nlica.ensure(std::max(nn, 1)));
+    HXC(cudaMemsetAsync(ctx->lib_nica.p, 0, sizeof(double) * std::max(nn, 1), st));
+    HXC(cudaMemsetAsync(ctx->lib_nlica.p, 0, sizeof(double) * std::max(nn, 1), st));
+    ctx->lib = true;
+    ctx->lib_nst = nst;
+    hx::DevLib& V = ctx->L;
+    V.nst = nst;
+    V.node_off = ctx->lib_node_off.p;
+    V.ent = ctx->lib_ent.p;
+    V.ent_st = ctx->lib_ent_st.p;
+    V.ent_fix = ctx->lib_ent_fix.p;
+    V.fix = ctx->lib_fix.p;
+    for (int k = 0; k < hx::kLibKinds; k++) V.prm[k] = ctx->prm[HX_P_CADYN_GAMMA + k].p;
+    V.st = ctx->lib_st.p;
+    V.lam = ctx->lib_lam.p;
+    V.nica = ctx->lib_nica.p;
+    V.nlica = ctx->lib_nlica.p;
+    V.dt = desc->dt;
+    // eion.cuh:38-41 with the 2018 CODATA constants of units.h
+    const double faraday = 1.602176634e-19 * 6.02214076e+23;
+    const double gas = 1.380649e-23 * 6.02214076e+23;
+    V.ktf = 1000. * gas * (desc->celsius + 273.15) / faraday;
+    return 0;
+}

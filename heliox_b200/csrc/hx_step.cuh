@@ -6,6 +6,7 @@
 #include <cuda_runtime.h>
 
 #include "hx_dev.hpp"
+#include "hx_lib.cuh"
 #include "hx_mech.cuh"
 
 namespace hx {
@@ -647,16 +648,19 @@ __device__ __forceinline__ double vjp_mech(const DevGroup& G, const DevGrad& GR,
 }
 
 // rhs/d of pack-local node i in the reference's accumulation order:
-// pas, hh, IClamp (CoreNEURON type order), [network currents], capacitance
+// pas, hh, IClamp (CoreNEURON type order), [network currents], [library
+// channels; *ica receives the node's calcium current], capacitance
 // jacobian, axial terms.  vi is the node's voltage; sv (neighbour voltages) is
 // read only when kRhs.
-template <bool kRhs, bool kNet = false, bool kSplitAxial = false>
+template <bool kRhs, bool kNet = false, bool kSplitAxial = false, bool kLib = false>
 __device__ __forceinline__ void assemble(const DevGroup& G, const Meta& M, int pb, int i, int fl, const NodePar& q,
                                          double vi, const double* __restrict__ sv, const double* __restrict__ sa,
                                          const double* __restrict__ sb, double m, double h, double n, double tmid,
                                          double& r_out, double& d_out, const DevNet& N = DevNet{},
                                          const double* synA = nullptr, const double* synB = nullptr, int syn0 = 0,
-                                         const double* grs = nullptr, const double* vpeer = nullptr) {
+                                         const double* grs = nullptr, const double* vpeer = nullptr,
+                                         const DevLib* L = nullptr, const double* X = nullptr,
+                                         double* ica = nullptr) {
     const int gi = pb + i;
     double r = 0.0, dd = 0.0;
     if (fl & kHasPas) {  // pas_templated.cu:27-31 through MechTemp::current (FD conductance)
@@ -680,6 +684,7 @@ __device__ __forceinline__ void assemble(const DevGroup& G, const Meta& M, int p
         r += cur * (1.e2 / __ldg(G.area + gi));
     }
     if (kNet) assemble_net(G, N, gi, vi, synA, synB, syn0, grs, vpeer, r, dd);
+    if (kLib) *ica = lib::lib_current(*L, gi, vi, X, r, dd);  // library types follow the network ones
     dd += G.cfac * q.cm;
     if (kSplitAxial) {  // parent / children may sit in other CTAs (a split cell)
         r_out = r;

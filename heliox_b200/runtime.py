@@ -37,6 +37,11 @@ _MECH_VAR = {
     ("gapjunction_lr", "w"): "gapjunction_lr.w",
     ("neuron_to_neuron_syn_lr", "w"): "neuron_to_neuron_syn_lr.w",
 }
+# library mechanisms: every HX_P key "<mech>.<var>" is also its handle name
+for _k in _lib.HX_P:
+    _m, _, _v = _k.partition(".")
+    if _m in ("CaDynamics_E2", "Ca_HVA", "Ca_LVAst", "Im", "K_Pst", "K_Tst", "NaTg", "Nap_Et2", "SK_E2", "SKv3_1"):
+        _MECH_VAR[(_m, _v)] = _k
 _HANDLE_SHIFT = 24
 
 
@@ -142,6 +147,9 @@ class Sim:
                "HalfGap": g.halfgap, "gapjunction_lr": g.gapjunction, "neuron_to_neuron_syn_lr": g.graded}.get(mech)
         if key == "cm":
             return g.nnode
+        if tab is None:
+            lt = g.lib.get(mech)
+            return lt.n if lt is not None else 0
         return tab.n
 
     # ------------------------------------------------------------------ network

@@ -20,7 +20,7 @@
 extern "C" {
 #endif
 
-#define HX_ABI_VERSION 2
+#define HX_ABI_VERSION 3
 
 typedef struct hx_ctx hx_ctx;
 
@@ -29,6 +29,47 @@ typedef struct hx_ctx hx_ctx;
  * holds after data_format_trans (src/neuron.h:19-130,
  * src/io/coredat_to_innerdat.cpp:569-603).  Mechanism instance tables are
  * sorted by node like the reference's nodeindices. */
+/* Library mechanisms: the ions and the user-mech channel set, CoreNEURON
+ * types after the network mechanisms in this order (src/mech/eion.cuh,
+ * src/mech/user-mech/{CaDynamics_E2,CA_HVA,Ca_LVAst,Im,K_Pst,K_Tst,NaTg,
+ * Nap_Et2,SK_E2,SKv3_1}.cu through MechTemp, src/mech/mech_template.cuh:
+ * 589-767).  Each table holds n instances on sorted, distinct reference nodes;
+ * par holds the type's columns instance by instance (row-major):
+ *   HX_LIB_NA_ION: ena | HX_LIB_K_ION: ek
+ *   HX_LIB_CA_ION: cai (initial), cao, eca, nernst (1: eca from cai/cao at
+ *                  finitialize and every step, eion.cuh:155-186; 0: fixed eca)
+ *   HX_LIB_CADYN (CaDynamics_E2): gamma, decay, depth, minCai
+ *   HX_LIB_CA_HVA .. HX_LIB_SKV3_1: gbar (the mechanism's gXbar RANGE)
+ *   HX_LIB_NATG: gbar, vshifth, vshiftm, slopeh, slopem
+ *   HX_LIB_SK_E2: gbar, zTau (one value: the mechanism's GLOBAL)
+ * A channel needs its ion on its node (Na: NaTg, Nap_Et2; K: Im, K_Pst,
+ * K_Tst, SK_E2, SKv3_1; Ca: CaDynamics_E2, Ca_HVA, Ca_LVAst, SK_E2 (cai));
+ * na_ion / k_ion on an hh node carry hh's ena / ek. */
+enum hx_lib_type {
+    HX_LIB_NA_ION = 0,
+    HX_LIB_K_ION = 1,
+    HX_LIB_CA_ION = 2,
+    HX_LIB_CADYN = 3,
+    HX_LIB_CA_HVA = 4,
+    HX_LIB_CA_LVAST = 5,
+    HX_LIB_IM = 6,
+    HX_LIB_K_PST = 7,
+    HX_LIB_K_TST = 8,
+    HX_LIB_NATG = 9,
+    HX_LIB_NAP_ET2 = 10,
+    HX_LIB_SK_E2 = 11,
+    HX_LIB_SKV3_1 = 12,
+    HX_LIB_NTYPE = 13
+};
+typedef struct hx_lib_table {
+    int n;
+    const int* node;
+    const double* par;
+} hx_lib_table;
+typedef struct hx_lib_desc {
+    hx_lib_table t[HX_LIB_NTYPE];
+} hx_lib_desc;
+
 typedef struct hx_group_desc {
     int ncell, nnode;
     const int* parent;
@@ -81,6 +122,10 @@ typedef struct hx_group_desc {
     int ngraded;
     const int *gr_node, *gr_pre;
     const double *gr_w, *gr_delta, *gr_vth;
+
+    /* ---- library mechanisms (NULL = none; not combined with network parts
+     * or a cell split across CTAs) */
+    const hx_lib_desc* lib;
 } hx_group_desc;
 
 /* Parameter / gradient kinds (per mechanism instance; HX_P_CM per node). */
@@ -101,7 +146,21 @@ enum hx_param_kind {
     HX_P_GAPJ_G = 13,
     HX_P_GAPJ_W = 14,
     HX_P_GRADED_W = 15,
-    HX_P_COUNT = 16
+    /* library mechanisms: per instance of the table, reference order */
+    HX_P_CADYN_GAMMA = 16,
+    HX_P_CADYN_DECAY = 17,
+    HX_P_CADYN_DEPTH = 18,
+    HX_P_CADYN_MINCAI = 19,
+    HX_P_CA_HVA_G = 20,
+    HX_P_CA_LVAST_G = 21,
+    HX_P_IM_G = 22,
+    HX_P_K_PST_G = 23,
+    HX_P_K_TST_G = 24,
+    HX_P_NATG_G = 25,
+    HX_P_NAP_ET2_G = 26,
+    HX_P_SK_E2_G = 27,
+    HX_P_SKV3_1_G = 28,
+    HX_P_COUNT = 29
 };
 
 /* Statistics of the execution plan built at load time. */
