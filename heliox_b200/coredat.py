@@ -307,7 +307,8 @@ def read_coredat(path: str, file_id=None) -> CellGroup:
     read_phase2; src/io/read_coredat.cpp:258-1120): the node arrays, the
     capacitance, pas, na_ion / k_ion, hh, IClamp, ExpSyn, Exp2Syn, NetStim,
     HalfGap, gapjunction_lr and neuron_to_neuron_syn_lr instances, the
-    PreSyns and one NetCon per ExpSyn / Exp2Syn instance.  HalfGap sources
+    library mechanisms (ca_ion, CaDynamics_E2 and the user-mech channel set),
+    the PreSyns and one NetCon per ExpSyn / Exp2Syn instance.  HalfGap sources
     come from ``halfgap.i32`` when present.  A file with other mechanisms, more
     than one NetCon on a synapse instance, per-node initial voltages or
     playback vectors is rejected with a ValueError naming what is not
@@ -482,10 +483,60 @@ def read_coredat(path: str, file_id=None) -> CellGroup:
     if halfgap.n and os.path.exists(hg_path):
         pairs = np.fromfile(hg_path, dtype=np.int32).reshape(-1, 2)
         halfgap.ifields["src"][pairs[:, 0]] = pairs[:, 1]
+    lib = _read_lib(tabs, glob)
     g = CellGroup(ncell=int(ncell), parent=_i32(parent), a=_f64(a), b=_f64(b), area=_f64(area), cm=_f64(cm),
                   hh=hh, pas=pas, iclamp=iclamp, celsius=glob.get("celsius", 6.3), dt=glob.get("dt", 0.025),
                   v_init=float(v[0]) if n else -65.0, name=os.path.basename(os.path.normpath(path)),
                   expsyn=expsyn, exp2syn=exp2syn, netstim=netstim, halfgap=halfgap, gapjunction=gapj,
-                  graded=graded, ps_thresh=_f64(ps_thresh))
+                  graded=graded, ps_thresh=_f64(ps_thresh), lib=lib)
     g.validate()
     return g
+
+
+def _read_lib(tabs, glob):
+    """Library tables of a read group: the channels and CaDynamics_E2 from
+    their data columns, ca_ion from the ion layout (eion.cuh:81-86) and its
+    iontype (04: default concentrations at finitialize, 040 / 0100: Nernst
+    eca at finitialize / every step, eion.cuh:155-186), na_ion / k_ion on the
+    nodes of the library channels that use them."""
+    import math
+
+    from .model import LIB_IONS, MechTable, _f64, _i32
+
+    lib = {}
+    for name, cols in LIB_COLUMNS.items():
+        if name not in tabs:
+            continue
+        nodes, data, _ = tabs[name]
+        fl = {key: _f64(data[:, c]) for key, c in cols.items()}
+        if name == "SK_E2":
+            if "zTau_SK_E2" not in glob:
+                raise ValueError("SK_E2 needs the GLOBAL zTau_SK_E2 in globals.dat")
+            fl["zTau"] = _f64(np.full(nodes.size, glob["zTau_SK_E2"]))
+        lib[name] = MechTable(_i32(nodes), fl)
+    if not lib:
+        return lib
+    if "ca_ion" in tabs:
+        nodes, data, pdata = tabs["ca_ion"]
+        it = pdata[:, 0] if pdata is not None else np.zeros(nodes.size, np.int32)
+        eca, cai, cao = data[:, 0].copy(), data[:, 1].copy(), data[:, 2].copy()
+        dflt = (it & 0o4) != 0
+        cai[dflt], cao[dflt] = 5.e-5, 2.0
+        every = (it & 0o100) != 0
+        once = ((it & 0o40) != 0) & ~every
+        if once.any():  # Nernst at finitialize only: a fixed eca from the initial concentrations
+            ktf = 1000. * (1.380649e-23 * 6.02214076e+23) * (glob.get("celsius", 6.3) + 273.15) / (
+                1.602176634e-19 * 6.02214076e+23)
+            for j in np.nonzero(once)[0]:
+                eca[j] = 1e6 if cai[j] <= 0. else -1e6 if cao[j] <= 0. else ktf / 2.0 * math.log(cao[j] / cai[j])
+        lib["ca_ion"] = MechTable(_i32(nodes), {"cai": _f64(cai), "cao": _f64(cao), "eca": _f64(eca)},
+                                  {"nernst": _i32(every.astype(np.int32))})
+    for ion, key, tag in (("na_ion", "ena", "na"), ("k_ion", "ek", "k")):
+        users = [lib[m].nodes for m, ions in LIB_IONS.items() if m in lib and tag in ions]
+        if not users or ion not in tabs:
+            continue
+        want = np.unique(np.concatenate(users))
+        nodes, data, _ = tabs[ion]
+        keep = np.isin(nodes, want)
+        lib[ion] = MechTable(_i32(nodes[keep]), {key: _f64(data[keep, 0])})
+    return lib

@@ -3,7 +3,8 @@
 ``write_coredat`` writes the files the reference's loader reads (checked by
 running the reference on them, tests/test_oracle_pin.py); ``read_coredat``
 reads them back.  A write -> read round trip must give back every node array,
-every mechanism table and the network wiring exactly.
+every mechanism table (library mechanisms included) and the network wiring
+exactly.
 """
 import os
 
@@ -27,6 +28,14 @@ def _same(g, h):
             assert np.array_equal(v, y.fields[k]), (t, k)
         for k, v in x.ifields.items():
             assert np.array_equal(v, y.ifields[k]), (t, k)
+    assert sorted(g.lib) == sorted(h.lib)
+    for t, x in g.lib.items():
+        y = h.lib[t]
+        assert np.array_equal(x.nodes, y.nodes), t
+        for k, v in x.fields.items():
+            assert np.array_equal(v, y.fields[k]), (t, k)
+        for k, v in x.ifields.items():
+            assert np.array_equal(v, y.ifields[k]), (t, k)
 
 
 @pytest.mark.parametrize(
@@ -36,12 +45,22 @@ def _same(g, h):
         lambda: synth.random_tree_batch(6, seed0=17),
         lambda: synth.spiking_network(),
         lambda: synth.coupled_network(),
+        lambda: synth.lib_tree_batch(2, seed0=8, nmax=150),
+        lambda: _lib_mixed(),
     ],
 )
 def test_write_read_round_trip(maker, tmp_path):
     g = maker()
     path = coredat.write_coredat(g, str(tmp_path / "model"))
     _same(g, coredat.read_coredat(path))
+
+
+def _lib_mixed():
+    from heliox_b200.model import concat_groups
+
+    g = concat_groups([synth.lib_tree_cell(4, ncomp=60), synth.random_tree_cell(5, ncomp=70)])
+    g.lib["ca_ion"].ifields["nernst"][::2] = 0  # fixed eca on every other calcium node
+    return g
 
 
 def test_read_needs_a_group_id_for_several_groups(tmp_path):
