@@ -7,7 +7,7 @@ against a teacher trace (conductances perturbed lognormally, sigma 0.2) and the
 reverse sweep producing every per-compartment conductance gradient.  The
 metric is forward+backward compartment-timesteps per second.
 
-  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--config 2|3|4|5]
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--config 2|3|4|5|6]
 
 Multi-GPU runs are launched by torchrun, one process per GPU; every rank
 integrates its own 1024-cell batch (cells are independent: weak scaling, no
@@ -23,7 +23,12 @@ The other configurations of the same metric (not the headline line):
                N x ncell cells, sharded by cell, spikes all-gathered over NCCL
                once per minimum-delay window (weak scaling);
   --config 5   302 cells coupled by 900 HalfGap pairs and 2000 graded
-               synapses, 8000 steps (one step per launch).
+               synapses, 8000 steps (one step per launch);
+  --config 6   library cells: --ncell random trees (default 1024, config-2
+               morphology) carrying the user-mech channel set with calcium
+               dynamics (NaTg, Nap_Et2, K_Pst, K_Tst, SKv3_1, SK_E2, Im,
+               Ca_HVA, Ca_LVAst, CaDynamics_E2, ions) and pas, 4000 steps,
+               gradients of every channel density and CaDynamics_E2 gamma.
 """
 from __future__ import annotations
 
@@ -67,6 +72,12 @@ def _alg_bytes(g):
     pas[g.pas.nodes] = True
     p = 3 + 4 * hh + 2 * pas
     s = 1 + 3 * hh
+    # library mechanisms: their states and parameters per instance (ions: erev / cai, cao)
+    from heliox_b200.model import LIB_FIELDS, LIB_STATES
+
+    for nm, tab in g.lib.items():
+        np.add.at(s, tab.nodes, len(LIB_STATES.get(nm, ())))
+        np.add.at(p, tab.nodes, len(LIB_FIELDS[nm]))
     fwd = 8 * (p + 2 * s) + 4
     tot = 8 * (3 * p + 8 * s) + 12
     # event synapses: 2 states, 2 parameters each (188 B per instance-step)
@@ -503,6 +514,17 @@ def build_workload(args, ws, rank):
                 "workload": f"config5: {g.ncell} cells, {g.halfgap.n // 2} HalfGap pairs, {g.graded.n} graded "
                             f"synapses, {T} steps, soma MSE vs teacher, gap and synapse gradients",
                 "parallelism": "replicas only ({ws} GPU(s)): coupled every step"}
+    if args.config == 6:
+        seed0 = 51000 + 100000 * rank
+        g = synth.lib_tree_batch(args.ncell, seed0=seed0, nmin=200, nmax=1000)
+        keys = ("NaTg.gNaTgbar", "Nap_Et2.gNap_Et2bar", "K_Pst.gK_Pstbar", "K_Tst.gK_Tstbar", "SKv3_1.gSKv3_1bar",
+                "SK_E2.gSK_E2bar", "Im.gImbar", "Ca_HVA.gbar", "Ca_LVAst.gCa_LVAstbar", "CaDynamics_E2.gamma")
+        return {"group": g, "teacher": synth.perturb_lib(g, 0.2, seed=seed0 + 7), "nstep": args.nstep, "keys": keys,
+                "probes": g.soma_nodes(),
+                "workload": f"config6: {args.ncell} seeded random-tree library cells per GPU (user-mech channel set "
+                            f"+ CaDynamics_E2 + pas, IClamp), {args.nstep} steps dt 0.025 ms, soma-MSE vs lognormal "
+                            "teacher, forward + exact adjoint",
+                "parallelism": "cells sharded, {ws} GPU(s), no collective on the data path"}
     raise ValueError(f"unknown config {args.config}")
 
 
@@ -515,7 +537,7 @@ def main():
     ap.add_argument("--ncell", type=int, default=NCELL)
     ap.add_argument("--nstep", type=int, default=T_STEPS)
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU-baseline leg")
-    ap.add_argument("--config", type=int, default=2, choices=(2, 3, 4, 5))
+    ap.add_argument("--config", type=int, default=2, choices=(2, 3, 4, 5, 6))
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
