@@ -184,21 +184,41 @@ HXD double log(double x) { return ::log(x); }
 HXD double pow(double x, double c) { return ::pow(x, c); }
 
 // ------------------------------------------------------------ shared forms
-// cnexp update of NaTg, Nap_Et2, SKv3_1, SK_E2, Im, K_Pst, K_Tst, Ca_LVAst:
-// x + (1 - exp(dt (-1/tau))) (-(inf/tau) / (-1/tau) - x)
-template <class T, class U>
-HXD T cnexp(const T& x, const T& inf, const U& tau, double dt) {
-    return x + (1.0 - exp(dt * (-1.0 / tau))) * (-(inf / tau) / (-1.0 / tau) - x);
+// The device forms below are the reference's formulas with its divisions
+// replaced by a Newton reciprocal (rcp_nz, hx_mech.cuh) or a multiplication
+// by a constant's reciprocal, reciprocal pairs exp(x), exp(-x) taken from one
+// exponential, and the cnexp update without its redundant divisions:
+//   x + (1 - exp(dt (-1/tau))) (-(inf/tau) / (-1/tau) - x)
+//     = x + (1 - exp(-dt / tau)) (inf - x).
+// They equal the reference's formulas mathematically and differ by rounding
+// only; oracle/hx_oracle_lib.c keeps the reference's exact operation order,
+// and the GPU path is checked against it within the voltage tolerance.
+__device__ __forceinline__ double rcp(double x) { return rcp_nz(x); }
+template <int N>
+__device__ __forceinline__ Dual<N> rcp(const Dual<N>& a) {
+    Dual<N> r;
+    r.v = rcp_nz(a.v);
+    const double s = -r.v * r.v;
+#pragma unroll
+    for (int i = 0; i < N; ++i) r.d[i] = s * a.d[i];
+    return r;
 }
 
-HXD double qt23() { return ::pow(2.3, ((34.0 - 21.0) / 10.0)); }
+template <class T>
+__device__ __forceinline__ T cnexp(const T& x, const T& inf, const T& tau, double dt) {
+    return x + (1.0 - exp(-dt * rcp(tau))) * (inf - x);
+}
+
+// 1 / pow(2.3, (34 - 21) / 10): the channels' temperature factor (their rates
+// divide by qt = 2.952882641412121...)
+constexpr double kIqt = 1.0 / 0x1.79f80ef2e5449p+1;
 
 // Nernst potential of a divalent ion (eion.cuh:38-56 with z = 2)
 template <class T>
-HXD T nernst2(const T& ci, double co, double ktf) {
+__device__ __forceinline__ T nernst2(const T& ci, double co, double ktf) {
     if (val(ci) <= 0.) return T(1e6);
     if (co <= 0.) return T(-1e6);
-    return ktf / 2.0 * log(co / ci);
+    return (ktf * 0.5) * log(co * rcp(ci));
 }
 
 // ------------------------------------------------------------ channels
@@ -208,39 +228,44 @@ HXD T nernst2(const T& ci, double co, double ktf) {
 // current_single_node returns; state(v, dt, s, f, cai) the state update;
 // init the INITIAL block.
 
-// NaTg.cu:78-160
+// NaTg.cu:78-160.  exp(-(-v + c)/slope) = 1 / exp(-(v - c)/slope).
 struct NaTg {
     static constexpr int kS = 2, kP = 1, kIon = 0;
     static constexpr bool kCai = false;
     template <class T>
-    HXD static void rates(const T& v, const double* f, T r[4]) {
-        const double qt = qt23();
+    __device__ static void rates(const T& v, const double* f, T r[4]) {
         const double vshifth = f[0], vshiftm = f[1], slopeh = f[2], slopem = f[3];
         T v_m = v;
         if (val(v_m) == -38.0) v_m = v_m + 0.0001;
-        const T mA = (0.182 * (v_m - (-38.0 + vshiftm))) / (1.0 - exp(-(v_m - (-38.0 + vshiftm)) / slopem));
-        const T mB = (0.124 * (-v_m + (-38.0 + vshiftm))) / (1.0 - exp(-(-v_m + (-38.0 + vshiftm)) / slopem));
-        r[1] = (1.0 / (mA + mB)) / qt;
-        r[0] = mA / (mA + mB);
+        const T xm = v_m - (-38.0 + vshiftm);
+        const T em = exp(-xm * rcp(slopem));
+        const T mA = (0.182 * xm) * rcp(1.0 - em);
+        const T mB = (0.124 * (-xm)) * rcp(1.0 - rcp(em));
+        const T rm = rcp(mA + mB);
+        r[1] = rm * kIqt;
+        r[0] = mA * rm;
         T v_h = v;
         if (val(v_h) == -66.0) v_h = v_h + 0.0001;
-        const T hA = (-0.015 * (v_h - (-66.0 + vshifth))) / (1.0 - exp((v_h - (-66.0 + vshifth)) / slopeh));
-        const T hB = (-0.015 * (-v_h + (-66.0 + vshifth))) / (1.0 - exp((-v_h + (-66.0 + vshifth)) / slopeh));
-        r[3] = (1.0 / (hA + hB)) / qt;
-        r[2] = hA / (hA + hB);
+        const T xh = v_h - (-66.0 + vshifth);
+        const T eh = exp(xh * rcp(slopeh));
+        const T hA = (-0.015 * xh) * rcp(1.0 - eh);
+        const T hB = (-0.015 * (-xh)) * rcp(1.0 - rcp(eh));
+        const T rh = rcp(hA + hB);
+        r[3] = rh * kIqt;
+        r[2] = hA * rh;
     }
     template <class T>
-    HXD static T cur(const T& v, const T* s, const T* p, const double*, const T& e) {
+    __device__ static T cur(const T& v, const T* s, const T* p, const double*, const T& e) {
         return p[0] * s[0] * s[0] * s[0] * s[1] * (v - e);
     }
     template <class T>
-    HXD static void state(const T& v, double dt, T* s, const double* f, const T&) {
+    __device__ static void state(const T& v, double dt, T* s, const double* f, const T&) {
         T r[4];
         rates(v, f, r);
         s[0] = cnexp(s[0], r[0], r[1], dt);
         s[1] = cnexp(s[1], r[2], r[3], dt);
     }
-    HXD static void init(double v, double* s, const double* f, double) {
+    __device__ static void init(double v, double* s, const double* f, double) {
         double r[4];
         rates(v, f, r);
         s[0] = r[0];
@@ -248,40 +273,41 @@ struct NaTg {
     }
 };
 
-// Nap_Et2.cu
+// Nap_Et2.cu.  exp(-(-v - 38)/6) = 1 / exp(-(v + 38)/6).
 struct NapEt2 {
     static constexpr int kS = 2, kP = 1, kIon = 0;
     static constexpr bool kCai = false;
     template <class T>
-    HXD static void rates(const T& v, T r[4]) {
-        const double qt = qt23();
-        r[0] = 1.0 / (1.0 + exp((v - (-52.6)) / (-4.6)));
+    __device__ static void rates(const T& v, T r[4]) {
+        r[0] = rcp(1.0 + exp((v - (-52.6)) * (1.0 / -4.6)));
         T v_m = v;
         if (val(v_m) == -38.0) v_m = v_m + 0.0001;
-        const T mA = (0.182 * (v_m - (-38.0))) / (1.0 - exp(-(v_m - (-38.0)) / 6.0));
-        const T mB = (0.124 * (-v_m - 38.0)) / (1.0 - exp(-(-v_m - 38.0) / 6.0));
-        r[1] = 6.0 * (1.0 / (mA + mB)) / qt;
+        const T xm = v_m - (-38.0);
+        const T em = exp(-xm * (1.0 / 6.0));
+        const T mA = (0.182 * xm) * rcp(1.0 - em);
+        const T mB = (0.124 * (-xm)) * rcp(1.0 - rcp(em));
+        r[1] = (6.0 * kIqt) * rcp(mA + mB);
         T v_h1 = v;
         if (val(v_h1) == -17.0) v_h1 = v_h1 + 0.0001;
         T v_h2 = v;
         if (val(v_h2) == -64.4) v_h2 = v_h2 + 0.0001;
-        r[2] = 1.0 / (1.0 + exp((v - (-48.8)) / 10.0));
-        const T hA = -2.88e-6 * (v_h1 + 17.0) / (1.0 - exp((v_h1 + 17.0) / 4.63));
-        const T hB = 6.94e-6 * (v_h2 + 64.4) / (1.0 - exp(-(v_h2 + 64.4) / 2.63));
-        r[3] = (1.0 / (hA + hB)) / qt;
+        r[2] = rcp(1.0 + exp((v - (-48.8)) * 0.1));
+        const T hA = (-2.88e-6 * (v_h1 + 17.0)) * rcp(1.0 - exp((v_h1 + 17.0) * (1.0 / 4.63)));
+        const T hB = (6.94e-6 * (v_h2 + 64.4)) * rcp(1.0 - exp(-(v_h2 + 64.4) * (1.0 / 2.63)));
+        r[3] = rcp(hA + hB) * kIqt;
     }
     template <class T>
-    HXD static T cur(const T& v, const T* s, const T* p, const double*, const T& e) {
+    __device__ static T cur(const T& v, const T* s, const T* p, const double*, const T& e) {
         return p[0] * s[0] * s[0] * s[0] * s[1] * (v - e);
     }
     template <class T>
-    HXD static void state(const T& v, double dt, T* s, const double*, const T&) {
+    __device__ static void state(const T& v, double dt, T* s, const double*, const T&) {
         T r[4];
         rates(v, r);
         s[0] = cnexp(s[0], r[0], r[1], dt);
         s[1] = cnexp(s[1], r[2], r[3], dt);
     }
-    HXD static void init(double v, double* s, const double*, double) {
+    __device__ static void init(double v, double* s, const double*, double) {
         double r[4];
         rates(v, r);
         s[0] = r[0];
@@ -294,29 +320,29 @@ struct KPst {
     static constexpr int kS = 2, kP = 1, kIon = 1;
     static constexpr bool kCai = false;
     template <class T>
-    HXD static void rates(const T& v_param, T r[4]) {
-        const double qt = qt23();
+    __device__ static void rates(const T& v_param, T r[4]) {
         const T v = v_param + 10.0;
-        r[0] = (1.0 / (1.0 + exp(-(v + 1.0) / 12.0)));
+        r[0] = rcp(1.0 + exp(-(v + 1.0) * (1.0 / 12.0)));
         if (val(v) < -50.0)
-            r[1] = (1.25 + 175.03 * exp(-v * (-0.026))) / qt;
+            r[1] = (1.25 + 175.03 * exp(v * 0.026)) * kIqt;
         else
-            r[1] = ((1.25 + 13.0 * exp(-v * 0.026))) / qt;
-        r[2] = 1.0 / (1.0 + exp(-(v + 54.0) / (-11.0)));
-        r[3] = (360.0 + (1010.0 + 24.0 * (v + 55.0)) * exp(-pow(((v + 75.0) / 48.0), 2.0))) / qt;
+            r[1] = (1.25 + 13.0 * exp(-v * 0.026)) * kIqt;
+        r[2] = rcp(1.0 + exp((v + 54.0) * (1.0 / 11.0)));
+        const T y = (v + 75.0) * (1.0 / 48.0);
+        r[3] = (360.0 + (1010.0 + 24.0 * (v + 55.0)) * exp(-(y * y))) * kIqt;
     }
     template <class T>
-    HXD static T cur(const T& v, const T* s, const T* p, const double*, const T& e) {
+    __device__ static T cur(const T& v, const T* s, const T* p, const double*, const T& e) {
         return p[0] * s[0] * s[0] * s[1] * (v - e);
     }
     template <class T>
-    HXD static void state(const T& v, double dt, T* s, const double*, const T&) {
+    __device__ static void state(const T& v, double dt, T* s, const double*, const T&) {
         T r[4];
         rates(v, r);
         s[0] = cnexp(s[0], r[0], r[1], dt);
         s[1] = cnexp(s[1], r[2], r[3], dt);
     }
-    HXD static void init(double v, double* s, const double*, double) {
+    __device__ static void init(double v, double* s, const double*, double) {
         double r[4];
         rates(v, r);
         s[0] = r[0];
@@ -324,31 +350,33 @@ struct KPst {
     }
 };
 
-// K_Tst.cu
+// K_Tst.cu (m^4 as two squarings)
 struct KTst {
     static constexpr int kS = 2, kP = 1, kIon = 1;
     static constexpr bool kCai = false;
     template <class T>
-    HXD static void rates(const T& v_param, T r[4]) {
-        const double qt = qt23();
+    __device__ static void rates(const T& v_param, T r[4]) {
         const T v = v_param + 10.0;
-        r[0] = 1.0 / (1.0 + exp(-(v + 0.0) / 19.0));
-        r[1] = (0.34 + 0.92 * exp(-pow(((v + 71.0) / 59.0), 2.0))) / qt;
-        r[2] = 1.0 / (1.0 + exp(-(v + 66.0) / (-10.0)));
-        r[3] = (8.0 + 49.0 * exp(-pow(((v + 73.0) / 23.0), 2.0))) / qt;
+        r[0] = rcp(1.0 + exp(-v * (1.0 / 19.0)));
+        const T y1 = (v + 71.0) * (1.0 / 59.0);
+        r[1] = (0.34 + 0.92 * exp(-(y1 * y1))) * kIqt;
+        r[2] = rcp(1.0 + exp((v + 66.0) * 0.1));
+        const T y2 = (v + 73.0) * (1.0 / 23.0);
+        r[3] = (8.0 + 49.0 * exp(-(y2 * y2))) * kIqt;
     }
     template <class T>
-    HXD static T cur(const T& v, const T* s, const T* p, const double*, const T& e) {
-        return p[0] * pow(s[0], 4.0) * s[1] * (v - e);
+    __device__ static T cur(const T& v, const T* s, const T* p, const double*, const T& e) {
+        const T m2 = s[0] * s[0];
+        return p[0] * (m2 * m2) * s[1] * (v - e);
     }
     template <class T>
-    HXD static void state(const T& v, double dt, T* s, const double*, const T&) {
+    __device__ static void state(const T& v, double dt, T* s, const double*, const T&) {
         T r[4];
         rates(v, r);
         s[0] = cnexp(s[0], r[0], r[1], dt);
         s[1] = cnexp(s[1], r[2], r[3], dt);
     }
-    HXD static void init(double v, double* s, const double*, double) {
+    __device__ static void init(double v, double* s, const double*, double) {
         double r[4];
         rates(v, r);
         s[0] = r[0];
@@ -361,26 +389,25 @@ struct CaLVAst {
     static constexpr int kS = 2, kP = 1, kIon = 2;
     static constexpr bool kCai = false;
     template <class T>
-    HXD static void rates(const T& v_param, T r[4]) {
-        const double qt = qt23();
+    __device__ static void rates(const T& v_param, T r[4]) {
         const T v = v_param + 10.0;
-        r[0] = 1.0 / (1.0 + exp((v - (-30.0)) / (-6.0)));
-        r[1] = (5.0 + 20.0 / (1.0 + exp((v - (-25.0)) / 5.0))) / qt;
-        r[2] = 1.0 / (1.0 + exp((v - (-80.0)) / 6.4));
-        r[3] = (20.0 + 50.0 / (1.0 + exp((v - (-40.0)) / 7.0))) / qt;
+        r[0] = rcp(1.0 + exp((v - (-30.0)) * (1.0 / -6.0)));
+        r[1] = (5.0 + 20.0 * rcp(1.0 + exp((v - (-25.0)) * 0.2))) * kIqt;
+        r[2] = rcp(1.0 + exp((v - (-80.0)) * (1.0 / 6.4)));
+        r[3] = (20.0 + 50.0 * rcp(1.0 + exp((v - (-40.0)) * (1.0 / 7.0)))) * kIqt;
     }
     template <class T>
-    HXD static T cur(const T& v, const T* s, const T* p, const double*, const T& e) {
+    __device__ static T cur(const T& v, const T* s, const T* p, const double*, const T& e) {
         return p[0] * s[0] * s[0] * s[1] * (v - e);
     }
     template <class T>
-    HXD static void state(const T& v, double dt, T* s, const double*, const T&) {
+    __device__ static void state(const T& v, double dt, T* s, const double*, const T&) {
         T r[4];
         rates(v, r);
         s[0] = cnexp(s[0], r[0], r[1], dt);
         s[1] = cnexp(s[1], r[2], r[3], dt);
     }
-    HXD static void init(double v, double* s, const double*, double) {
+    __device__ static void init(double v, double* s, const double*, double) {
         double r[4];
         rates(v, r);
         s[0] = r[0];
@@ -393,34 +420,37 @@ struct CaHVA {
     static constexpr int kS = 2, kP = 1, kIon = 2;
     static constexpr bool kCai = false;
     template <class T>
-    HXD static T vtrap(const T& x, double y) {
-        if (fabs(val(x) / y) < 1e-6) return y * (1.0 - x / y / 2.0);
-        return x / (exp(x / y) - 1.0);
+    __device__ static T vtrap38(const T& x) {  // vtrap(x, 3.8)
+        const T u = x * (1.0 / 3.8);
+        if (fabs(val(u)) < 1e-6) return 3.8 * (1.0 - u * 0.5);
+        return x * rcp(exp(u) - 1.0);
     }
     template <class T>
-    HXD static void rates(const T& v, T r[4]) {
-        const T mA = 0.055 * vtrap(-27.0 - v, 3.8);
-        const T mB = 0.94 * exp((-75.0 - v) / 17.0);
-        r[0] = mA / (mA + mB);
-        r[1] = 1.0 / (mA + mB);
-        const T hA = 0.000457 * exp((-13.0 - v) / 50.0);
-        const T hB = 0.0065 / (exp((-v - 15.0) / 28.0) + 1.0);
-        r[2] = hA / (hA + hB);
-        r[3] = 1.0 / (hA + hB);
+    __device__ static void rates(const T& v, T r[4]) {
+        const T mA = 0.055 * vtrap38(-27.0 - v);
+        const T mB = 0.94 * exp((-75.0 - v) * (1.0 / 17.0));
+        const T rm = rcp(mA + mB);
+        r[0] = mA * rm;
+        r[1] = rm;
+        const T hA = 0.000457 * exp((-13.0 - v) * 0.02);
+        const T hB = 0.0065 * rcp(exp((-v - 15.0) * (1.0 / 28.0)) + 1.0);
+        const T rh = rcp(hA + hB);
+        r[2] = hA * rh;
+        r[3] = rh;
     }
     template <class T>
-    HXD static T cur(const T& v, const T* s, const T* p, const double*, const T& e) {
+    __device__ static T cur(const T& v, const T* s, const T* p, const double*, const T& e) {
         const T g = p[0] * s[0] * s[0] * s[1];
         return g * (v - e);
     }
     template <class T>
-    HXD static void state(const T& v, double dt, T* s, const double*, const T&) {
+    __device__ static void state(const T& v, double dt, T* s, const double*, const T&) {
         T r[4];
         rates(v, r);
-        s[0] = s[0] + (1.0 - exp(-dt / r[1])) * (r[0] - s[0]);
-        s[1] = s[1] + (1.0 - exp(-dt / r[3])) * (r[2] - s[1]);
+        s[0] = cnexp(s[0], r[0], r[1], dt);
+        s[1] = cnexp(s[1], r[2], r[3], dt);
     }
-    HXD static void init(double v, double* s, const double*, double) {
+    __device__ static void init(double v, double* s, const double*, double) {
         double r[4];
         rates(v, r);
         s[0] = r[0];
@@ -428,29 +458,30 @@ struct CaHVA {
     }
 };
 
-// Im.cu
+// Im.cu.  exp(-0.1 (v + 35)) = 1 / exp(0.1 (v + 35)).
 struct Im {
     static constexpr int kS = 1, kP = 1, kIon = 1;
     static constexpr bool kCai = false;
     template <class T>
-    HXD static void rates(const T& v, T r[2]) {
-        const double qt = qt23();
-        const T mA = 3.3e-3 * exp(2.5 * 0.04 * (v - (-35.0)));
-        const T mB = 3.3e-3 * exp(-2.5 * 0.04 * (v - (-35.0)));
-        r[0] = mA / (mA + mB);
-        r[1] = (1.0 / (mA + mB)) / qt;
+    __device__ static void rates(const T& v, T r[2]) {
+        const T e = exp((2.5 * 0.04) * (v - (-35.0)));
+        const T mA = 3.3e-3 * e;
+        const T mB = 3.3e-3 * rcp(e);
+        const T rs = rcp(mA + mB);
+        r[0] = mA * rs;
+        r[1] = rs * kIqt;
     }
     template <class T>
-    HXD static T cur(const T& v, const T* s, const T* p, const double*, const T& e) {
+    __device__ static T cur(const T& v, const T* s, const T* p, const double*, const T& e) {
         return p[0] * s[0] * (v - e);
     }
     template <class T>
-    HXD static void state(const T& v, double dt, T* s, const double*, const T&) {
+    __device__ static void state(const T& v, double dt, T* s, const double*, const T&) {
         T r[2];
         rates(v, r);
         s[0] = cnexp(s[0], r[0], r[1], dt);
     }
-    HXD static void init(double v, double* s, const double*, double) {
+    __device__ static void init(double v, double* s, const double*, double) {
         double r[2];
         rates(v, r);
         s[0] = r[0];
@@ -462,21 +493,21 @@ struct SKv31 {
     static constexpr int kS = 1, kP = 1, kIon = 1;
     static constexpr bool kCai = false;
     template <class T>
-    HXD static void rates(const T& v, T r[2]) {
-        r[0] = 1.0 / (1.0 + exp((v - 18.700) / (-9.700)));
-        r[1] = 0.2 * 20.0 / (1.0 + exp((v - (-46.560)) / (-44.140)));
+    __device__ static void rates(const T& v, T r[2]) {
+        r[0] = rcp(1.0 + exp((v - 18.700) * (1.0 / -9.700)));
+        r[1] = (0.2 * 20.0) * rcp(1.0 + exp((v - (-46.560)) * (1.0 / -44.140)));
     }
     template <class T>
-    HXD static T cur(const T& v, const T* s, const T* p, const double*, const T& e) {
+    __device__ static T cur(const T& v, const T* s, const T* p, const double*, const T& e) {
         return p[0] * s[0] * (v - e);
     }
     template <class T>
-    HXD static void state(const T& v, double dt, T* s, const double*, const T&) {
+    __device__ static void state(const T& v, double dt, T* s, const double*, const T&) {
         T r[2];
         rates(v, r);
         s[0] = cnexp(s[0], r[0], r[1], dt);
     }
-    HXD static void init(double v, double* s, const double*, double) {
+    __device__ static void init(double v, double* s, const double*, double) {
         double r[2];
         rates(v, r);
         s[0] = r[0];
@@ -488,29 +519,32 @@ struct SKE2 {
     static constexpr int kS = 1, kP = 1, kIon = 1;
     static constexpr bool kCai = true;
     template <class T>
-    HXD static T zinf(const T& ca) {
+    __device__ static T zinf(const T& ca) {
         T ca_safe = ca;
         if (val(ca_safe) < 1e-7) ca_safe = ca_safe + 1e-07;
-        return 1.0 / (1.0 + pow((0.00043 / ca_safe), 4.8));
+        return rcp(1.0 + pow(0.00043 * rcp(ca_safe), 4.8));
     }
     template <class T>
-    HXD static T cur(const T& v, const T* s, const T* p, const double*, const T& e) {
+    __device__ static T cur(const T& v, const T* s, const T* p, const double*, const T& e) {
         return p[0] * s[0] * (v - e);
     }
     template <class T>
-    HXD static void state(const T&, double dt, T* s, const double* f, const T& cai) {
-        s[0] = cnexp(s[0], zinf(cai), f[0], dt);
+    __device__ static void state(const T&, double dt, T* s, const double* f, const T& cai) {
+        s[0] = s[0] + (1.0 - exp(-dt * rcp(f[0]))) * (zinf(cai) - s[0]);
     }
-    HXD static void init(double, double* s, const double*, double cai) { s[0] = zinf(cai); }
+    __device__ static void init(double, double* s, const double*, double cai) { s[0] = zinf(cai); }
 };
 
-// CaDynamics_E2.cu:101-137: cai' from cai and the step's calcium current
+// CaDynamics_E2.cu:101-137: cai' from cai and the step's calcium current.
+// The reference's steady term -(drive - (-minCai)/decay) / (-1/decay)
+// equals drive decay + minCai.
 template <class T>
-HXD T cadyn(const T& cai, const T& ica, const T& gamma, const T& decay, const T& depth, const T& minCai, double dt) {
+__device__ __forceinline__ T cadyn(const T& cai, const T& ica, const T& gamma, const T& decay, const T& depth,
+                                   const T& minCai, double dt) {
     const double FARADAY = 96485.3321233100184;
-    const T drive_ica = -(10000.0) * (ica * gamma) / (2.0 * FARADAY * depth);
-    const T exp_factor = exp(dt * (-1.0 / decay));
-    const T steady_term = -(drive_ica - (-minCai) / decay) / (-1.0 / decay);
+    const T drive_ica = (-10000.0 * (ica * gamma)) * rcp((2.0 * FARADAY) * depth);
+    const T exp_factor = exp(-dt * rcp(decay));
+    const T steady_term = drive_ica * decay + minCai;
     return cai + (1.0 - exp_factor) * (steady_term - cai);
 }
 
