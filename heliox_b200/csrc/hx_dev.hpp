@@ -139,6 +139,7 @@ constexpr int kLibKinds = 13;
 struct DevLib {
     int nst;
     const int *node_off, *ent, *ent_st, *ent_fix;  // node_off: nnode + 1; ent_st: nent + 1
+    const unsigned short* mask;  // per node: bit t set when the node has an entry of type t
     const double* fix;
     const double* prm[kLibKinds];
     double* grad[kLibKinds];

@@ -232,7 +232,6 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_kernel(DevGroup G, DevState S
         // C: v update (the gates follow in the next step's A, or below)
         for (int i = i0 + g.tl; i < i1; i += g.nt) {
             sv[i] = sv[i] + srhs[i];
-            if (kLib) lib::lib_state(L, pb + i, sv[i], L.st);
             if (kNet) {  // synapse decay x + c (0 - x) (expsyn.cpp:125-134, exp2syn_temp.cuh:51-58)
                 const int s1 = __ldg(N.node_syn_off + pb + i + 1);
                 for (int j = __ldg(N.node_syn_off + pb + i); j < s1; ++j) {
@@ -242,6 +241,8 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_kernel(DevGroup G, DevState S
                 }
             }
         }
+        // library states at the new v, type by type over this thread's nodes
+        if (kLib) lib::lib_state_cell(L, pb, i0, i1, g.tl, g.nt, sv);
         g.sync();
         if (trace)
             for (int q = q0 + g.tl; q < q1; q += g.nt) trace[(size_t)(k + 1) * P.nprobe + P.slot[q]] = sv[P.local[q]];

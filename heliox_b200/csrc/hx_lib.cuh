@@ -222,11 +222,14 @@ __device__ __forceinline__ T nernst2(const T& ci, double co, double ktf) {
 }
 
 // ------------------------------------------------------------ channels
-// Each channel: kS states, kP trainable parameters (the density gbar), the
+// Each channel: kS gates, kP trainable parameters (the density gbar), the
 // ion it reads erev of and writes its current to (0 Na, 1 K, 2 Ca), kCai when
-// its state update reads cai.  cur(v, s, p, f, e) is the value
-// current_single_node returns; state(v, dt, s, f, cai) the state update;
-// init the INITIAL block.
+// its gates depend on cai.  cur(v, s, p, f, e) is the value
+// current_single_node returns; gates(v, f, cai, r) gives every gate's steady
+// state and time constant (r[2j], r[2j+1]).  The reference's STATE blocks of
+// these channels are all the cnexp update of each gate toward its steady
+// state, and their INITIAL blocks set each gate to it (chan_state,
+// chan_init below).
 
 // NaTg.cu:78-160.  exp(-(-v + c)/slope) = 1 / exp(-(v - c)/slope).
 struct NaTg {
@@ -259,17 +262,8 @@ struct NaTg {
         return p[0] * s[0] * s[0] * s[0] * s[1] * (v - e);
     }
     template <class T>
-    __device__ static void state(const T& v, double dt, T* s, const double* f, const T&) {
-        T r[4];
+    __device__ static void gates(const T& v, const double* f, const T&, T* r) {
         rates(v, f, r);
-        s[0] = cnexp(s[0], r[0], r[1], dt);
-        s[1] = cnexp(s[1], r[2], r[3], dt);
-    }
-    __device__ static void init(double v, double* s, const double* f, double) {
-        double r[4];
-        rates(v, f, r);
-        s[0] = r[0];
-        s[1] = r[2];
     }
 };
 
@@ -301,17 +295,8 @@ struct NapEt2 {
         return p[0] * s[0] * s[0] * s[0] * s[1] * (v - e);
     }
     template <class T>
-    __device__ static void state(const T& v, double dt, T* s, const double*, const T&) {
-        T r[4];
+    __device__ static void gates(const T& v, const double*, const T&, T* r) {
         rates(v, r);
-        s[0] = cnexp(s[0], r[0], r[1], dt);
-        s[1] = cnexp(s[1], r[2], r[3], dt);
-    }
-    __device__ static void init(double v, double* s, const double*, double) {
-        double r[4];
-        rates(v, r);
-        s[0] = r[0];
-        s[1] = r[2];
     }
 };
 
@@ -336,17 +321,8 @@ struct KPst {
         return p[0] * s[0] * s[0] * s[1] * (v - e);
     }
     template <class T>
-    __device__ static void state(const T& v, double dt, T* s, const double*, const T&) {
-        T r[4];
+    __device__ static void gates(const T& v, const double*, const T&, T* r) {
         rates(v, r);
-        s[0] = cnexp(s[0], r[0], r[1], dt);
-        s[1] = cnexp(s[1], r[2], r[3], dt);
-    }
-    __device__ static void init(double v, double* s, const double*, double) {
-        double r[4];
-        rates(v, r);
-        s[0] = r[0];
-        s[1] = r[2];
     }
 };
 
@@ -370,17 +346,8 @@ struct KTst {
         return p[0] * (m2 * m2) * s[1] * (v - e);
     }
     template <class T>
-    __device__ static void state(const T& v, double dt, T* s, const double*, const T&) {
-        T r[4];
+    __device__ static void gates(const T& v, const double*, const T&, T* r) {
         rates(v, r);
-        s[0] = cnexp(s[0], r[0], r[1], dt);
-        s[1] = cnexp(s[1], r[2], r[3], dt);
-    }
-    __device__ static void init(double v, double* s, const double*, double) {
-        double r[4];
-        rates(v, r);
-        s[0] = r[0];
-        s[1] = r[2];
     }
 };
 
@@ -401,17 +368,8 @@ struct CaLVAst {
         return p[0] * s[0] * s[0] * s[1] * (v - e);
     }
     template <class T>
-    __device__ static void state(const T& v, double dt, T* s, const double*, const T&) {
-        T r[4];
+    __device__ static void gates(const T& v, const double*, const T&, T* r) {
         rates(v, r);
-        s[0] = cnexp(s[0], r[0], r[1], dt);
-        s[1] = cnexp(s[1], r[2], r[3], dt);
-    }
-    __device__ static void init(double v, double* s, const double*, double) {
-        double r[4];
-        rates(v, r);
-        s[0] = r[0];
-        s[1] = r[2];
     }
 };
 
@@ -444,17 +402,8 @@ struct CaHVA {
         return g * (v - e);
     }
     template <class T>
-    __device__ static void state(const T& v, double dt, T* s, const double*, const T&) {
-        T r[4];
+    __device__ static void gates(const T& v, const double*, const T&, T* r) {
         rates(v, r);
-        s[0] = cnexp(s[0], r[0], r[1], dt);
-        s[1] = cnexp(s[1], r[2], r[3], dt);
-    }
-    __device__ static void init(double v, double* s, const double*, double) {
-        double r[4];
-        rates(v, r);
-        s[0] = r[0];
-        s[1] = r[2];
     }
 };
 
@@ -476,15 +425,8 @@ struct Im {
         return p[0] * s[0] * (v - e);
     }
     template <class T>
-    __device__ static void state(const T& v, double dt, T* s, const double*, const T&) {
-        T r[2];
+    __device__ static void gates(const T& v, const double*, const T&, T* r) {
         rates(v, r);
-        s[0] = cnexp(s[0], r[0], r[1], dt);
-    }
-    __device__ static void init(double v, double* s, const double*, double) {
-        double r[2];
-        rates(v, r);
-        s[0] = r[0];
     }
 };
 
@@ -502,15 +444,8 @@ struct SKv31 {
         return p[0] * s[0] * (v - e);
     }
     template <class T>
-    __device__ static void state(const T& v, double dt, T* s, const double*, const T&) {
-        T r[2];
+    __device__ static void gates(const T& v, const double*, const T&, T* r) {
         rates(v, r);
-        s[0] = cnexp(s[0], r[0], r[1], dt);
-    }
-    __device__ static void init(double v, double* s, const double*, double) {
-        double r[2];
-        rates(v, r);
-        s[0] = r[0];
     }
 };
 
@@ -529,10 +464,10 @@ struct SKE2 {
         return p[0] * s[0] * (v - e);
     }
     template <class T>
-    __device__ static void state(const T&, double dt, T* s, const double* f, const T& cai) {
-        s[0] = s[0] + (1.0 - exp(-dt * rcp(f[0]))) * (zinf(cai) - s[0]);
+    __device__ static void gates(const T&, const double* f, const T& cai, T* r) {
+        r[0] = zinf(cai);
+        r[1] = T(f[0]);
     }
-    __device__ static void init(double, double* s, const double*, double cai) { s[0] = zinf(cai); }
 };
 
 // CaDynamics_E2.cu:101-137: cai' from cai and the step's calcium current.
@@ -616,33 +551,50 @@ __device__ __forceinline__ double vjp_cur(double v, const double* s, const doubl
     return gr[0];
 }
 
+// A channel's state phase: each gate x' = x + (1 - exp(-dt/tau)) (inf - x)
+template <class M>
+__device__ __forceinline__ void chan_state(double v, double dt, double* s, const double* f, double cai) {
+    double r[2 * M::kS];
+    M::template gates<double>(v, f, cai, r);
+#pragma unroll
+    for (int j = 0; j < M::kS; ++j) s[j] = cnexp(s[j], r[2 * j], r[2 * j + 1], dt);
+}
+
+// INITIAL: every gate at its steady state
+template <class M>
+__device__ __forceinline__ void chan_init(double v, double* s, const double* f, double cai) {
+    double r[2 * M::kS];
+    M::template gates<double>(v, f, cai, r);
+#pragma unroll
+    for (int j = 0; j < M::kS; ++j) s[j] = r[2 * j];
+}
+
 // Adjoint of one channel's state update s_{k+1} = F(v_{k+1}, s_k[, cai_{k+1}]):
-// lam holds dL/ds_{k+1} on entry and dL/ds_k (through F) on return; returns
-// dL/dv_{k+1} through F and adds dL/dcai_{k+1} to lcai.
+// lam holds dL/ds_{k+1} on entry and dL/ds_k on return (d x'/d x = exp(-dt/tau));
+// returns dL/dv_{k+1} and adds dL/dcai_{k+1} to lcai.  The gates' steady
+// states and time constants depend on v (and cai) only, so they are
+// evaluated with one or two dual lanes.
 template <class M>
 __device__ __forceinline__ double vjp_state(double v1, double dt, const double* s, const double* f, double cai,
                                             double* lam, double& lcai) {
-    constexpr int N = 1 + M::kS + (M::kCai ? 1 : 0);
+    constexpr int N = M::kCai ? 2 : 1;
     using D = Dual<N>;
-    D ds[M::kS];
-#pragma unroll
-    for (int i = 0; i < M::kS; ++i) ds[i] = D::var(s[i], 1 + i);
     const D dv = D::var(v1, 0);
     const D dc = M::kCai ? D::var(cai, N - 1) : D(cai);
-    M::template state<D>(dv, dt, ds, f, dc);
-    double acc[N];
-#pragma unroll
-    for (int k = 0; k < N; ++k) acc[k] = 0.0;
+    D r[2 * M::kS];
+    M::template gates<D>(dv, f, dc, r);
+    double mu = 0.0;
 #pragma unroll
     for (int j = 0; j < M::kS; ++j) {
+        const D E = exp(-dt * rcp(r[2 * j + 1]));
+        const double x = s[j];
+        const D y = x + (1.0 - E) * (r[2 * j] - x);
         const double l = lam[j];
-#pragma unroll
-        for (int k = 0; k < N; ++k) acc[k] += l * ds[j].d[k];
+        mu += l * y.d[0];
+        if (M::kCai) lcai += l * y.d[N - 1];
+        lam[j] = l * E.v;
     }
-#pragma unroll
-    for (int i = 0; i < M::kS; ++i) lam[i] = acc[1 + i];
-    if (M::kCai) lcai += acc[N - 1];
-    return acc[0];
+    return mu;
 }
 
 __device__ __forceinline__ int entry_type(int code) { return code >> 24; }
@@ -690,34 +642,43 @@ __device__ __forceinline__ double lib_current(const DevLib& L, int gi, double v,
     return ica;
 }
 
-// State phase of GPU node gi at the new voltage v: CaDynamics_E2 (from the
-// step's calcium current nica) before the channels, then the channels in type
-// order, updating X in place.
-__device__ __forceinline__ void lib_state(const DevLib& L, int gi, double v, double* X) {
-    const int e0 = __ldg(L.node_off + gi), e1 = __ldg(L.node_off + gi + 1);
-    int cs = -1;
-    for (int e = e0; e < e1; ++e) {
-        const int code = __ldg(L.ent + e), t = entry_type(code), inst = entry_inst(code);
-        double* s = X + __ldg(L.ent_st + e);
-        const double* f = L.fix + __ldg(L.ent_fix + e);
-        switch (t) {
-            case kCaIon:
-                cs = __ldg(L.ent_st + e);
-                break;
-            case kCaDyn:
-                X[cs] = cadyn<double>(X[cs], L.nica[gi], __ldg(L.prm[0] + inst), __ldg(L.prm[1] + inst),
-                                      __ldg(L.prm[2] + inst), __ldg(L.prm[3] + inst), L.dt);
-                break;
-#define HX_LIB_ST(T_, M_)                                                    \
-    case T_:                                                                 \
-        M_::template state<double>(v, L.dt, s, f, cs >= 0 ? X[cs] : 0.0);   \
-        break;
-                HX_LIB_CHANNELS(HX_LIB_ST)
-#undef HX_LIB_ST
-            default:
-                break;
-        }
+// State phase of the nodes [i0, i1) of a cell that this thread owns (i0 +
+// tl, step nt), mechanism type by mechanism type: CaDynamics_E2 first (from
+// the step's calcium current L.nica), then the channels in type order at the
+// new voltage -- per node the reference's order (nonvint_cpu), and each pass
+// runs one mechanism's code over all the thread's nodes (shorter live
+// ranges: the forward kernel's spills drop from ~1 KB to under 100 B a
+// thread).  sv: the new voltages, pb: the pack's first GPU node.
+template <int T, class M>
+__device__ __forceinline__ void lib_state_type(const DevLib& L, int pb, int i0, int i1, int tl, int nt,
+                                               const double* sv) {
+    for (int i = i0 + tl; i < i1; i += nt) {
+        const int gi = pb + i;
+        const unsigned m = __ldg(L.mask + gi);
+        if (!(m & (1u << T))) continue;
+        const int e0 = __ldg(L.node_off + gi);
+        const int e = e0 + __popc(m & ((1u << T) - 1u));
+        double cai = 0.0;
+        if (M::kCai) cai = L.st[__ldg(L.ent_st + e0 + __popc(m & ((1u << kCaIon) - 1u)))];
+        chan_state<M>(sv[i], L.dt, L.st + __ldg(L.ent_st + e), L.fix + __ldg(L.ent_fix + e), cai);
     }
+}
+
+__device__ __forceinline__ void lib_state_cell(const DevLib& L, int pb, int i0, int i1, int tl, int nt,
+                                               const double* sv) {
+    for (int i = i0 + tl; i < i1; i += nt) {
+        const int gi = pb + i;
+        const unsigned m = __ldg(L.mask + gi);
+        if (!(m & (1u << kCaDyn))) continue;
+        const int e = __ldg(L.node_off + gi) + __popc(m & ((1u << kCaDyn) - 1u));
+        const int inst = entry_inst(__ldg(L.ent + e));
+        double* cai = L.st + __ldg(L.ent_st + e - 1);  // the node's ca_ion entry precedes CaDynamics_E2
+        *cai = cadyn<double>(*cai, L.nica[gi], __ldg(L.prm[0] + inst), __ldg(L.prm[1] + inst),
+                             __ldg(L.prm[2] + inst), __ldg(L.prm[3] + inst), L.dt);
+    }
+#define HX_LIB_STT(T_, M_) lib_state_type<T_, M_>(L, pb, i0, i1, tl, nt, sv);
+    HX_LIB_CHANNELS(HX_LIB_STT)
+#undef HX_LIB_STT
 }
 
 // finitialize of GPU node gi at v: ca_ion's initial cai, the channels' INITIAL
@@ -736,7 +697,7 @@ __device__ __forceinline__ void lib_init(const DevLib& L, int gi, double v) {
                 break;
 #define HX_LIB_INIT(T_, M_)       \
     case T_:                      \
-        M_::init(v, s, f, cai);   \
+        chan_init<M_>(v, s, f, cai);   \
         break;
                 HX_LIB_CHANNELS(HX_LIB_INIT)
 #undef HX_LIB_INIT

@@ -114,6 +114,7 @@ int hx_lib_load(hx_ctx* ctx, const hx_group_desc* desc) {
         if (!(D->t[HX_LIB_CA_ION].par[4 * j] > 0.0)) return fail(ctx, "ca_ion: cai must be positive");
     // entries in GPU node order, types ascending on a node
     std::vector<int> node_off(nn + 1, 0), ent, ent_st, ent_fix;
+    std::vector<unsigned short> mask(std::max(nn, 1), 0);
     std::vector<double> fix;
     std::vector<int> inst(HX_LIB_NTYPE, 0);
     std::vector<std::vector<double>> prm(hx::kLibKinds);
@@ -129,6 +130,7 @@ int hx_lib_load(hx_ctx* ctx, const hx_group_desc* desc) {
             const int ntr = L::ntrain(t), nfx = L::nfix(t), q = inst[t]++;
             const double* par = D->t[t].par + (size_t)(ntr + nfx) * j;
             ent.push_back(t << 24 | q);
+            mask[gi] |= (unsigned short)(1u << t);
             ent_st.push_back(nst);
             nst += L::nstate(t);
             ent_fix.push_back((int)fix.size());
@@ -151,6 +153,7 @@ int hx_lib_load(hx_ctx* ctx, const hx_group_desc* desc) {
         if (D->t[HX_LIB_SK_E2].par[2 * j + 1] != sk_tau)
             return fail(ctx, "SK_E2: zTau is a GLOBAL of the mechanism, one value for all instances");
     HXC(ctx->lib_node_off.upload(node_off, st));
+    HXC(ctx->lib_mask.upload(mask, st));
     HXC(ctx->lib_ent.upload(ent, st));
     HXC(ctx->lib_ent_st.upload(ent_st, st));
     HXC(ctx->lib_ent_fix.upload(ent_fix, st));
@@ -170,6 +173,7 @@ int hx_lib_load(hx_ctx* ctx, const hx_group_desc* desc) {
     hx::DevLib& V = ctx->L;
     V.nst = nst;
     V.node_off = ctx->lib_node_off.p;
+    V.mask = ctx->lib_mask.p;
     V.ent = ctx->lib_ent.p;
     V.ent_st = ctx->lib_ent_st.p;
     V.ent_fix = ctx->lib_ent_fix.p;
