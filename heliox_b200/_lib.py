@@ -47,9 +47,11 @@ HX_P = {
     "Nap_Et2.gNap_Et2bar": 26,
     "SK_E2.gSK_E2bar": 27,
     "SKv3_1.gSKv3_1bar": 28,
+    "hd_la.ghdbar": 29,
+    "km_la.gbar": 30,
 }
-HX_P_COUNT = 29
-HX_LIB_NTYPE = 13
+HX_P_COUNT = 31
+HX_LIB_NTYPE = 15
 
 
 class LibTable(C.Structure):

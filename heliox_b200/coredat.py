@@ -35,7 +35,7 @@ from typing import List, Tuple
 
 import numpy as np
 
-from .model import CellGroup
+from .model import LIB_GLOBALS, CellGroup
 
 VERSION = "1.8"
 
@@ -71,6 +71,8 @@ LIB_MECH_TABLE: List[Tuple[int, str, int, int, int, int, int, float]] = [
     (23, "Nap_Et2", 0, 0, 0, 5, 0, 0.0),
     (24, "SK_E2", 0, 0, 0, 4, 0, 0.0),
     (25, "SKv3_1", 0, 0, 0, 4, 0, 0.0),
+    (26, "hd_la", 0, 0, 0, 11, 0, 0.0),
+    (27, "km_la", 0, 0, 0, 13, 0, 0.0),
 ]
 # data column of each library field (its var_in_coredata_idx); SK_E2.zTau is
 # the GLOBAL zTau_SK_E2 of globals.dat (SK_E2.cu:65-66)
@@ -80,7 +82,11 @@ LIB_COLUMNS = {
     "K_Tst": {"gK_Tstbar": 0},
     "NaTg": {"gNaTgbar": 0, "vshifth": 1, "vshiftm": 2, "slopeh": 3, "slopem": 4},
     "Nap_Et2": {"gNap_Et2bar": 0}, "SK_E2": {"gSK_E2bar": 0}, "SKv3_1": {"gSKv3_1bar": 0},
+    "hd_la": {"ghdbar": 0, "vhalfl": 1, "tau": 2}, "km_la": {"gbar": 0},
 }
+# GLOBALs the loader requires of a mechanism that the dynamics do not read
+# (km_la.cu:70-80: its table parameters), written with these values
+LIB_EXTRA_GLOBALS = {"km_la": {"temp": 23.0, "q10": 2.3, "vmin": -120.0, "vmax": 100.0, "usetable": 0.0}}
 # ca_ion iontype with Nernst reversal potentials at finitialize and every step
 # (eion.cuh:165, 181: bits 040 and 0100)
 IONTYPE_NERNST = 0o140
@@ -130,9 +136,14 @@ def write_coredat(g: CellGroup, path: str, file_id: int = 0) -> str:
         f.write(f"{VERSION}\n")
         f.write(f"celsius {g.celsius:.17g}\n")
         f.write(f"dt {g.dt:.17g}\n")
-        sk = g.lib.get("SK_E2")
-        if sk is not None and sk.n:
-            f.write(f"zTau_SK_E2 {float(sk.fields['zTau'][0]):.17g}\n")
+        for nm, keys in LIB_GLOBALS.items():
+            tab = g.lib.get(nm)
+            if tab is None or not tab.n:
+                continue
+            for k in keys:
+                f.write(f"{k}_{nm} {float(tab.fields[k][0]):.17g}\n")
+            for k, val in LIB_EXTRA_GLOBALS.get(nm, {}).items():
+                f.write(f"{k}_{nm} {val:.17g}\n")
         f.write("0 0\n")
         f.write("secondorder 0\n")
 
@@ -509,10 +520,10 @@ def _read_lib(tabs, glob):
             continue
         nodes, data, _ = tabs[name]
         fl = {key: _f64(data[:, c]) for key, c in cols.items()}
-        if name == "SK_E2":
-            if "zTau_SK_E2" not in glob:
-                raise ValueError("SK_E2 needs the GLOBAL zTau_SK_E2 in globals.dat")
-            fl["zTau"] = _f64(np.full(nodes.size, glob["zTau_SK_E2"]))
+        for k in LIB_GLOBALS.get(name, ()):
+            if f"{k}_{name}" not in glob:
+                raise ValueError(f"{name} needs the GLOBAL {k}_{name} in globals.dat")
+            fl[k] = _f64(np.full(nodes.size, glob[f"{k}_{name}"]))
         lib[name] = MechTable(_i32(nodes), fl)
     if not lib:
         return lib

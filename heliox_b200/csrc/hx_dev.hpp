@@ -132,10 +132,12 @@ struct DevNet {
 // type << 24 | instance (GPU instance order of its type), its states at
 // ent_st[e] of the flat state array (ca_ion: cai; channels: their gates) and
 // its fixed parameters at ent_fix[e] of fix (ions: erev / concentrations;
-// NaTg: vshifth, vshiftm, slopeh, slopem; SK_E2: zTau).  Trainable
-// parameters (HX_P_CADYN_GAMMA .. HX_P_SKV3_1_G) live per instance in
+// NaTg: vshifth, vshiftm, slopeh, slopem; SK_E2: zTau; hd_la: vhalfl, tau,
+// ehd, kl, vhalft, a0t, zetat, gmt and qtl q10^((celsius - 33)/10) a0t;
+// km_la: Ra, Rb, tha, qa, tadj).  Trainable
+// parameters (HX_P_CADYN_GAMMA .. HX_P_KM_LA_G) live per instance in
 // prm[kind - HX_P_CADYN_GAMMA], their gradients in grad[...].
-constexpr int kLibKinds = 13;
+constexpr int kLibKinds = 15;
 struct DevLib {
     int nst;
     const int *node_off, *ent, *ent_st, *ent_fix;  // node_off: nnode + 1; ent_st: nent + 1

@@ -223,7 +223,8 @@ __device__ __forceinline__ T nernst2(const T& ci, double co, double ktf) {
 
 // ------------------------------------------------------------ channels
 // Each channel: kS gates, kP trainable parameters (the density gbar), the
-// ion it reads erev of and writes its current to (0 Na, 1 K, 2 Ca), kCai when
+// ion it reads erev of and writes its current to (0 Na, 1 K, 2 Ca; 3 none:
+// a nonspecific current with the reversal potential fix[kErevFix]), kCai when
 // its gates depend on cai.  cur(v, s, p, f, e) is the value
 // current_single_node returns; gates(v, f, cai, r) gives every gate's steady
 // state and time constant (r[2j], r[2j+1]).  The reference's STATE blocks of
@@ -235,6 +236,7 @@ __device__ __forceinline__ T nernst2(const T& ci, double co, double ktf) {
 struct NaTg {
     static constexpr int kS = 2, kP = 1, kIon = 0;
     static constexpr bool kCai = false;
+    static constexpr int kErevFix = 0;  // kIon 3: erev is fix[kErevFix]
     template <class T>
     __device__ static void rates(const T& v, const double* f, T r[4]) {
         const double vshifth = f[0], vshiftm = f[1], slopeh = f[2], slopem = f[3];
@@ -271,6 +273,7 @@ struct NaTg {
 struct NapEt2 {
     static constexpr int kS = 2, kP = 1, kIon = 0;
     static constexpr bool kCai = false;
+    static constexpr int kErevFix = 0;  // kIon 3: erev is fix[kErevFix]
     template <class T>
     __device__ static void rates(const T& v, T r[4]) {
         r[0] = rcp(1.0 + exp((v - (-52.6)) * (1.0 / -4.6)));
@@ -304,6 +307,7 @@ struct NapEt2 {
 struct KPst {
     static constexpr int kS = 2, kP = 1, kIon = 1;
     static constexpr bool kCai = false;
+    static constexpr int kErevFix = 0;  // kIon 3: erev is fix[kErevFix]
     template <class T>
     __device__ static void rates(const T& v_param, T r[4]) {
         const T v = v_param + 10.0;
@@ -330,6 +334,7 @@ struct KPst {
 struct KTst {
     static constexpr int kS = 2, kP = 1, kIon = 1;
     static constexpr bool kCai = false;
+    static constexpr int kErevFix = 0;  // kIon 3: erev is fix[kErevFix]
     template <class T>
     __device__ static void rates(const T& v_param, T r[4]) {
         const T v = v_param + 10.0;
@@ -355,6 +360,7 @@ struct KTst {
 struct CaLVAst {
     static constexpr int kS = 2, kP = 1, kIon = 2;
     static constexpr bool kCai = false;
+    static constexpr int kErevFix = 0;  // kIon 3: erev is fix[kErevFix]
     template <class T>
     __device__ static void rates(const T& v_param, T r[4]) {
         const T v = v_param + 10.0;
@@ -377,6 +383,7 @@ struct CaLVAst {
 struct CaHVA {
     static constexpr int kS = 2, kP = 1, kIon = 2;
     static constexpr bool kCai = false;
+    static constexpr int kErevFix = 0;  // kIon 3: erev is fix[kErevFix]
     template <class T>
     __device__ static T vtrap38(const T& x) {  // vtrap(x, 3.8)
         const T u = x * (1.0 / 3.8);
@@ -411,6 +418,7 @@ struct CaHVA {
 struct Im {
     static constexpr int kS = 1, kP = 1, kIon = 1;
     static constexpr bool kCai = false;
+    static constexpr int kErevFix = 0;  // kIon 3: erev is fix[kErevFix]
     template <class T>
     __device__ static void rates(const T& v, T r[2]) {
         const T e = exp((2.5 * 0.04) * (v - (-35.0)));
@@ -434,6 +442,7 @@ struct Im {
 struct SKv31 {
     static constexpr int kS = 1, kP = 1, kIon = 1;
     static constexpr bool kCai = false;
+    static constexpr int kErevFix = 0;  // kIon 3: erev is fix[kErevFix]
     template <class T>
     __device__ static void rates(const T& v, T r[2]) {
         r[0] = rcp(1.0 + exp((v - 18.700) * (1.0 / -9.700)));
@@ -453,6 +462,7 @@ struct SKv31 {
 struct SKE2 {
     static constexpr int kS = 1, kP = 1, kIon = 1;
     static constexpr bool kCai = true;
+    static constexpr int kErevFix = 0;  // kIon 3: erev is fix[kErevFix]
     template <class T>
     __device__ static T zinf(const T& ca) {
         T ca_safe = ca;
@@ -467,6 +477,53 @@ struct SKE2 {
     __device__ static void gates(const T&, const double* f, const T& cai, T* r) {
         r[0] = zinf(cai);
         r[1] = T(f[0]);
+    }
+};
+
+// hd_la.cu:86-124 (Ih, a nonspecific current with the GLOBAL reversal
+// potential ehd).  f: vhalfl, tau, ehd, kl, vhalft, a0t, zetat, gmt, c with
+// c = qtl q10^((celsius - 33)/10) a0t from the load.
+struct HdLa {
+    static constexpr int kS = 1, kP = 1, kIon = 3;
+    static constexpr bool kCai = false;
+    static constexpr int kErevFix = 2;
+    template <class T>
+    __device__ static T cur(const T& v, const T* s, const T* p, const double*, const T& e) {
+        const T ghd = p[0] * s[0];
+        return ghd * (v - e);
+    }
+    template <class T>
+    __device__ static void gates(const T& v, const double* f, const T&, T* r) {
+        const double vhalfl = f[0], tau = f[1], kl = f[3], vhalft = f[4], zetat = f[6], gmt = f[7], c = f[8];
+        const T x = v - vhalft;
+        const T a = exp((0.0378 * zetat) * x);
+        r[0] = rcp(1.0 + exp(-(v - vhalfl) * rcp(kl)));
+        r[1] = (tau * exp(((0.0378 * zetat) * gmt) * x)) * rcp(c * (1.0 + a));
+    }
+};
+
+// km_la.cu:97-145 (gbar in pS/um2; GLOBALs Ra, Rb, tha, qa, tadj).  The
+// update x + nexp (inf - x), nexp = 1 - exp(-dt tadj / ntau), is the cnexp
+// form with tau = ntau / tadj; exp((v - tha)/qa) = 1 / exp(-(v - tha)/qa).
+struct KmLa {
+    static constexpr int kS = 1, kP = 1, kIon = 1;
+    static constexpr bool kCai = false;
+    static constexpr int kErevFix = 0;
+    template <class T>
+    __device__ static T cur(const T& v, const T* s, const T* p, const double* f, const T& e) {
+        const T gk = f[4] * p[0] * s[0];
+        return (1e-4 * gk) * (v - e);
+    }
+    template <class T>
+    __device__ static void gates(const T& v, const double* f, const T&, T* r) {
+        const double Ra = f[0], Rb = f[1], tha = f[2], qa = f[3], tadj = f[4];
+        const T x = v - tha;
+        const T em = exp(-x * rcp(qa));
+        const T a = (Ra * x) * rcp(1.0 - em);
+        const T b = (-Rb * x) * rcp(1.0 - rcp(em));
+        const T rs = rcp(a + b);
+        r[0] = a * rs;
+        r[1] = rs * rcp(tadj);
     }
 };
 
@@ -485,7 +542,8 @@ __device__ __forceinline__ T cadyn(const T& cai, const T& ica, const T& gamma, c
 
 // ------------------------------------------------------------ type table
 enum LibType : int {
-    kNaIon = 0, kKIon, kCaIon, kCaDyn, kCaHVA, kCaLVAst, kIm, kKPst, kKTst, kNaTg, kNapEt2, kSKE2, kSKv31, kNType
+    kNaIon = 0, kKIon, kCaIon, kCaDyn, kCaHVA, kCaLVAst, kIm, kKPst, kKTst, kNaTg, kNapEt2, kSKE2, kSKv31, kHdLa,
+    kKmLa, kNType
 };
 // first trainable kind of each type, relative to HX_P_CADYN_GAMMA (-1: none)
 __host__ __device__ constexpr int kind0(int t) {
@@ -493,10 +551,12 @@ __host__ __device__ constexpr int kind0(int t) {
 }
 // states per entry / fixed parameters per entry / trainable parameters per instance
 __host__ __device__ constexpr int nstate(int t) {
-    return t == kCaIon ? 1 : (t == kIm || t == kSKE2 || t == kSKv31) ? 1 : t >= kCaHVA ? 2 : 0;
+    return t == kCaIon ? 1 : (t == kIm || t == kSKE2 || t == kSKv31 || t == kHdLa || t == kKmLa) ? 1
+                                                                                                : t >= kCaHVA ? 2 : 0;
 }
 __host__ __device__ constexpr int nfix(int t) {
-    return (t == kNaIon || t == kKIon) ? 1 : t == kCaIon ? 4 : t == kNaTg ? 4 : t == kSKE2 ? 1 : 0;
+    return (t == kNaIon || t == kKIon) ? 1 : t == kCaIon ? 4 : t == kNaTg ? 4 : t == kSKE2 ? 1 : t == kHdLa ? 9
+                                                                                 : t == kKmLa ? 5 : 0;
 }
 __host__ __device__ constexpr int ntrain(int t) { return t < kCaDyn ? 0 : t == kCaDyn ? 4 : 1; }
 
@@ -509,7 +569,9 @@ __host__ __device__ constexpr int ntrain(int t) { return t < kCaDyn ? 0 : t == k
     X(kNaTg, NaTg)         \
     X(kNapEt2, NapEt2)     \
     X(kSKE2, SKE2)         \
-    X(kSKv31, SKv31)
+    X(kSKv31, SKv31)       \
+    X(kHdLa, HdLa)         \
+    X(kKmLa, KmLa)
 
 // ------------------------------------------------------------ drivers
 // one channel's forward contribution; returns I(v) (the ion current)
@@ -629,7 +691,7 @@ __device__ __forceinline__ double lib_current(const DevLib& L, int gi, double v,
 #define HX_LIB_FWD(T_, M_)                                                          \
     case T_: {                                                                      \
         const double p[1] = {__ldg(L.prm[kind0(T_)] + inst)};                       \
-        const double e_ = M_::kIon == 0 ? ena : M_::kIon == 1 ? ek : eca;           \
+        const double e_ = M_::kIon == 0 ? ena : M_::kIon == 1 ? ek : M_::kIon == 2 ? eca : __ldg(f + M_::kErevFix); \
         const double i0 = fwd_cur<M_>(v, s, p, f, e_, r, dd);                       \
         if (M_::kIon == 2) ica += i0;                                               \
     } break;
@@ -790,7 +852,7 @@ __device__ __forceinline__ double lib_current_adj(const DevLib& L, int gi, doubl
 #define HX_LIB_CADJ(T_, M_)                                                                    \
     case T_: {                                                                                 \
         const double p[1] = {__ldg(L.prm[kind0(T_)] + inst)};                                  \
-        const double e_ = M_::kIon == 0 ? ena : M_::kIon == 1 ? ek : eca;                      \
+        const double e_ = M_::kIon == 0 ? ena : M_::kIon == 1 ? ek : M_::kIon == 2 ? eca : __ldg(f + M_::kErevFix); \
         double gp[1] = {0.0}, le = 0.0;                                                        \
         lv += vjp_cur<M_>(v, Xk + so, p, f, e_, w, ld, M_::kIon == 2 ? lica : 0.0, lam + so,   \
                           gp, le);                                                             \

@@ -1,6 +1,6 @@
 // hx_runtime_lib.cu -- host side of the library mechanisms (hx_lib.cuh):
 // the per-node entry tables in GPU order, the parameter kinds
-// HX_P_CADYN_GAMMA .. HX_P_SKV3_1_G, and the device arrays of DevLib.
+// HX_P_CADYN_GAMMA .. HX_P_KM_LA_G, and the device arrays of DevLib.
 //
 // The reference keeps one instance table per mechanism type
 // (MechTemp::reg_node_indices / read_data_from_coredat,
@@ -26,9 +26,13 @@ int fail(hx_ctx* c, const std::string& m) { return hx_fail(c, m); }
         if (_e != cudaSuccess) return fail(ctx, std::string(#call) + ": " + cudaGetErrorString(_e)); \
     } while (0)
 
-const char* kTypeName[HX_LIB_NTYPE] = {"na_ion",  "k_ion",  "ca_ion",  "CaDynamics_E2", "Ca_HVA",
-                                       "Ca_LVAst", "Im",     "K_Pst",   "K_Tst",         "NaTg",
-                                       "Nap_Et2",  "SK_E2",  "SKv3_1"};
+const char* kTypeName[HX_LIB_NTYPE] = {"na_ion", "k_ion", "ca_ion",  "CaDynamics_E2", "Ca_HVA",
+                                       "Ca_LVAst", "Im",   "K_Pst",   "K_Tst",         "NaTg",
+                                       "Nap_Et2", "SK_E2", "SKv3_1", "hd_la",         "km_la"};
+
+// columns of a type's hx_lib_table rows (trainable first, then fixed); hd_la's
+// GLOBALs q10 and qtl enter the device's fixed parameters as one factor
+int desc_cols(int t) { return t == HX_LIB_HD_LA ? 11 : hx::lib::ntrain(t) + hx::lib::nfix(t); }
 
 // ions a type needs on its node: bit 0 Na, 1 K, 2 Ca
 int ions_needed(int t) {
@@ -40,6 +44,7 @@ int ions_needed(int t) {
         case HX_LIB_K_PST:
         case HX_LIB_K_TST:
         case HX_LIB_SKV3_1:
+        case HX_LIB_KM_LA:
             return 2;
         case HX_LIB_SK_E2:
             return 2 | 4;
@@ -55,7 +60,7 @@ int ions_needed(int t) {
 
 int hx_lib_type_of_kind(int kind) {
     if (kind >= HX_P_CADYN_GAMMA && kind <= HX_P_CADYN_MINCAI) return HX_LIB_CADYN;
-    if (kind >= HX_P_CA_HVA_G && kind <= HX_P_SKV3_1_G) return kind - HX_P_CA_HVA_G + HX_LIB_CA_HVA;
+    if (kind >= HX_P_CA_HVA_G && kind <= HX_P_KM_LA_G) return kind - HX_P_CA_HVA_G + HX_LIB_CA_HVA;
     return -1;
 }
 
@@ -77,7 +82,7 @@ int hx_lib_load(hx_ctx* ctx, const hx_group_desc* desc) {
         }
     cudaStream_t st = ctx->st;
     if (!any) {
-        for (int k = HX_P_CADYN_GAMMA; k <= HX_P_SKV3_1_G; k++) {
+        for (int k = HX_P_CADYN_GAMMA; k <= HX_P_KM_LA_G; k++) {
             ctx->kmap_h[k].assign(1, 0);
             HXC(ctx->kmap[k].upload(ctx->kmap_h[k], st));
             HXC(ctx->prm[k].ensure(1));
@@ -119,7 +124,7 @@ int hx_lib_load(hx_ctx* ctx, const hx_group_desc* desc) {
     std::vector<int> inst(HX_LIB_NTYPE, 0);
     std::vector<std::vector<double>> prm(hx::kLibKinds);
     for (int k = 0; k < hx::kLibKinds; k++) prm[k].assign(1, 0.0);
-    for (int k = HX_P_CADYN_GAMMA; k <= HX_P_SKV3_1_G; k++)
+    for (int k = HX_P_CADYN_GAMMA; k <= HX_P_KM_LA_G; k++)
         ctx->kmap_h[k].assign(std::max(ctx->lib_n[hx_lib_type_of_kind(k)], 1), 0);
     int nst = 0;
     for (int gi = 0; gi < nn; gi++) {
@@ -128,13 +133,21 @@ int hx_lib_load(hx_ctx* ctx, const hx_group_desc* desc) {
             const int j = at[t][r];
             if (j < 0) continue;
             const int ntr = L::ntrain(t), nfx = L::nfix(t), q = inst[t]++;
-            const double* par = D->t[t].par + (size_t)(ntr + nfx) * j;
+            const double* par = D->t[t].par + (size_t)desc_cols(t) * j;
             ent.push_back(t << 24 | q);
             mask[gi] |= (unsigned short)(1u << t);
             ent_st.push_back(nst);
             nst += L::nstate(t);
             ent_fix.push_back((int)fix.size());
-            for (int c = 0; c < nfx; c++) fix.push_back(par[ntr + c]);
+            if (t == HX_LIB_HD_LA) {
+                // vhalfl, tau, ehd, kl, vhalft, a0t, zetat, gmt, then qtl * qt * a0t with
+                // qt = pow(q10, (celsius - 33) / 10) as hd_la.cu:94 computes it
+                for (int c = 1; c <= 8; c++) fix.push_back(par[c]);
+                const double qt = std::pow(par[9], ((desc->celsius - 33.0) / 10.0));
+                fix.push_back(par[10] * qt * par[6]);
+            } else {
+                for (int c = 0; c < nfx; c++) fix.push_back(par[ntr + c]);
+            }
             const int k0 = L::kind0(t);
             for (int c = 0; c < ntr; c++) {
                 std::vector<double>& pv = prm[k0 + c];
@@ -148,17 +161,24 @@ int hx_lib_load(hx_ctx* ctx, const hx_group_desc* desc) {
     ent_st.push_back(nst);
     if (fix.empty()) fix.push_back(0.0);
     if (ent.empty()) ent.push_back(0);
-    const double sk_tau = D->t[HX_LIB_SK_E2].n ? D->t[HX_LIB_SK_E2].par[1] : 0.0;
-    for (int j = 1; j < D->t[HX_LIB_SK_E2].n; j++)
-        if (D->t[HX_LIB_SK_E2].par[2 * j + 1] != sk_tau)
-            return fail(ctx, "SK_E2: zTau is a GLOBAL of the mechanism, one value for all instances");
+    // GLOBALs of a mechanism: one value over its instances
+    const int glo_t[3] = {HX_LIB_SK_E2, HX_LIB_HD_LA, HX_LIB_KM_LA}, glo_c0[3] = {1, 3, 1};
+    for (int u = 0; u < 3; u++) {
+        const hx_lib_table& T = D->t[glo_t[u]];
+        const int nc = desc_cols(glo_t[u]);
+        for (int j = 1; j < T.n; j++)
+            for (int c = glo_c0[u]; c < nc; c++)
+                if (T.par[(size_t)nc * j + c] != T.par[c])
+                    return fail(ctx, std::string(kTypeName[glo_t[u]]) +
+                                         ": a GLOBAL of the mechanism differs between instances");
+    }
     HXC(ctx->lib_node_off.upload(node_off, st));
     HXC(ctx->lib_mask.upload(mask, st));
     HXC(ctx->lib_ent.upload(ent, st));
     HXC(ctx->lib_ent_st.upload(ent_st, st));
     HXC(ctx->lib_ent_fix.upload(ent_fix, st));
     HXC(ctx->lib_fix.upload(fix, st));
-    for (int k = HX_P_CADYN_GAMMA; k <= HX_P_SKV3_1_G; k++) {
+    for (int k = HX_P_CADYN_GAMMA; k <= HX_P_KM_LA_G; k++) {
         HXC(ctx->kmap[k].upload(ctx->kmap_h[k], st));
         HXC(ctx->prm[k].upload(prm[k - HX_P_CADYN_GAMMA], st));
     }

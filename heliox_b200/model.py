@@ -82,7 +82,16 @@ LIB_MECHS = (
     ("Nap_Et2", ("gNap_Et2bar",), 1),
     ("SK_E2", ("gSK_E2bar", "zTau"), 1),
     ("SKv3_1", ("gSKv3_1bar",), 1),
+    ("hd_la", ("ghdbar", "vhalfl", "tau", "ehd", "kl", "vhalft", "a0t", "zetat", "gmt", "q10", "qtl"), 1),
+    ("km_la", ("gbar", "Ra", "Rb", "tha", "qa", "tadj"), 1),
 )
+# fields that are GLOBALs of their mechanism in the reference (one value per
+# group, written to globals.dat as <field>_<mechanism>)
+LIB_GLOBALS = {
+    "SK_E2": ("zTau",),
+    "hd_la": ("ehd", "kl", "vhalft", "a0t", "zetat", "gmt", "q10", "qtl"),
+    "km_la": ("Ra", "Rb", "tha", "qa", "tadj"),
+}
 LIB_NAMES = tuple(m[0] for m in LIB_MECHS)
 LIB_FIELDS = {m[0]: m[1] for m in LIB_MECHS}
 LIB_NTRAIN = {m[0]: m[2] for m in LIB_MECHS}
@@ -90,6 +99,7 @@ LIB_NTRAIN = {m[0]: m[2] for m in LIB_MECHS}
 LIB_IONS = {
     "CaDynamics_E2": ("ca",), "Ca_HVA": ("ca",), "Ca_LVAst": ("ca",), "Im": ("k",), "K_Pst": ("k",),
     "K_Tst": ("k",), "NaTg": ("na",), "Nap_Et2": ("na",), "SK_E2": ("k", "ca"), "SKv3_1": ("k",),
+    "hd_la": (), "km_la": ("k",),
 }
 
 
@@ -290,9 +300,13 @@ class CellGroup:
             common, ia, ib = np.intersect1d(it.nodes, self.hh.nodes, return_indices=True)
             if common.size and not np.array_equal(it.fields[key][ia], self.hh.fields[key][ib]):
                 raise ValueError(f"{ion}.{key} differs from hh.{key} on a shared node")
-        sk = self.lib.get("SK_E2")
-        if sk is not None and sk.n and np.any(sk.fields["zTau"] != sk.fields["zTau"][0]):
-            raise ValueError("SK_E2.zTau is a GLOBAL of the mechanism: one value for all instances")
+        for nm, keys in LIB_GLOBALS.items():
+            tab = self.lib.get(nm)
+            if tab is None or not tab.n:
+                continue
+            for k in keys:
+                if np.any(tab.fields[k] != tab.fields[k][0]):
+                    raise ValueError(f"{nm}.{k} is a GLOBAL of the mechanism: one value for all instances")
 
     def copy(self) -> "CellGroup":
         return CellGroup(
@@ -358,7 +372,8 @@ def lib_par_matrix(g: "CellGroup", name: str) -> np.ndarray:
 
 # states per library table, in the order the forward keeps them
 LIB_STATES = {"ca_ion": ("cai",), "Ca_HVA": ("m", "h"), "Ca_LVAst": ("m", "h"), "Im": ("m",), "K_Pst": ("m", "h"),
-              "K_Tst": ("m", "h"), "NaTg": ("m", "h"), "Nap_Et2": ("m", "h"), "SK_E2": ("z",), "SKv3_1": ("m",)}
+              "K_Tst": ("m", "h"), "NaTg": ("m", "h"), "Nap_Et2": ("m", "h"), "SK_E2": ("z",), "SKv3_1": ("m",),
+              "hd_la": ("l",), "km_la": ("n",)}
 
 
 def empty_table(names, inames=()) -> MechTable:

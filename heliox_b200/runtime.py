@@ -40,7 +40,8 @@ _MECH_VAR = {
 # library mechanisms: every HX_P key "<mech>.<var>" is also its handle name
 for _k in _lib.HX_P:
     _m, _, _v = _k.partition(".")
-    if _m in ("CaDynamics_E2", "Ca_HVA", "Ca_LVAst", "Im", "K_Pst", "K_Tst", "NaTg", "Nap_Et2", "SK_E2", "SKv3_1"):
+    if _m in ("CaDynamics_E2", "Ca_HVA", "Ca_LVAst", "Im", "K_Pst", "K_Tst", "NaTg", "Nap_Et2", "SK_E2", "SKv3_1",
+              "hd_la", "km_la"):
         _MECH_VAR[(_m, _v)] = _k
 _HANDLE_SHIFT = 24
 

@@ -241,6 +241,14 @@ LIB_DENSITY = {
     "Im": (0.0, 0.0, 1e-4),
     "Ca_HVA": (1e-3, 1e-3, 5e-5),
     "Ca_LVAst": (3e-3, 5e-3, 1e-4),
+    "hd_la": (5e-5, 0.0, 1e-4),
+    "km_la": (10.0, 20.0, 0.0),  # pS/um^2 (km_la.cu:53)
+}
+# GLOBALs of hd_la / km_la (one value per group; their published defaults,
+# km_la's tadj = 2.3^((34 - 23) / 10)) and hd_la's per-instance vhalfl, tau
+LIB_LA_GLOBALS = {
+    "hd_la": dict(ehd=-30.0, kl=-8.0, vhalft=-75.0, a0t=0.011, zetat=2.2, gmt=0.4, q10=4.5, qtl=1.0),
+    "km_la": dict(Ra=0.001, Rb=0.001, tha=-30.0, qa=9.0, tadj=2.3 ** 1.1),
 }
 LIB_CADYN = (dict(gamma=5e-4, decay=460.0), dict(gamma=5e-4, decay=100.0), dict(gamma=5e-4, decay=80.0))
 LIB_GBAR_FIELD = {nm: LIB_FIELDS[nm][0] for nm in LIB_DENSITY}
@@ -278,6 +286,10 @@ def lib_tree_cell(seed: int, ncomp: int | None = None, nmin: int = 100, nmax: in
                      slopeh=_f64(np.full(nodes.size, 6.0)), slopem=_f64(np.full(nodes.size, 6.0)))
         if nm == "SK_E2":
             f["zTau"] = _f64(np.ones(nodes.size))
+        if nm == "hd_la":
+            f.update(vhalfl=_f64(np.full(nodes.size, -81.0)), tau=_f64(np.ones(nodes.size)))
+        for k, val in LIB_LA_GLOBALS.get(nm, {}).items():
+            f[k] = _f64(np.full(nodes.size, val))
         lib[nm] = MechTable(_i32(nodes), f)
         for ion in LIB_IONS[nm]:
             need[ion][nodes] = True

@@ -32,7 +32,7 @@ typedef struct hx_ctx hx_ctx;
 /* Library mechanisms: the ions and the user-mech channel set, CoreNEURON
  * types after the network mechanisms in this order (src/mech/eion.cuh,
  * src/mech/user-mech/{CaDynamics_E2,CA_HVA,Ca_LVAst,Im,K_Pst,K_Tst,NaTg,
- * Nap_Et2,SK_E2,SKv3_1}.cu through MechTemp, src/mech/mech_template.cuh:
+ * Nap_Et2,SK_E2,SKv3_1,hd_la,km_la}.cu through MechTemp, src/mech/mech_template.cuh:
  * 589-767).  Each table holds n instances on sorted, distinct reference nodes;
  * par holds the type's columns instance by instance (row-major):
  *   HX_LIB_NA_ION: ena | HX_LIB_K_ION: ek
@@ -42,8 +42,13 @@ typedef struct hx_ctx hx_ctx;
  *   HX_LIB_CA_HVA .. HX_LIB_SKV3_1: gbar (the mechanism's gXbar RANGE)
  *   HX_LIB_NATG: gbar, vshifth, vshiftm, slopeh, slopem
  *   HX_LIB_SK_E2: gbar, zTau (one value: the mechanism's GLOBAL)
+ *   HX_LIB_HD_LA (hd_la.cu): ghdbar, vhalfl, tau, then its GLOBALs ehd, kl,
+ *                  vhalft, a0t, zetat, gmt, q10, qtl (one value each)
+ *   HX_LIB_KM_LA (km_la.cu): gbar (pS/um2), then its GLOBALs Ra, Rb, tha, qa,
+ *                  tadj (one value each)
  * A channel needs its ion on its node (Na: NaTg, Nap_Et2; K: Im, K_Pst,
- * K_Tst, SK_E2, SKv3_1; Ca: CaDynamics_E2, Ca_HVA, Ca_LVAst, SK_E2 (cai));
+ * K_Tst, SK_E2, SKv3_1, km_la; Ca: CaDynamics_E2, Ca_HVA, Ca_LVAst, SK_E2
+ * (cai)); hd_la's current is nonspecific (its own ehd);
  * na_ion / k_ion on an hh node carry hh's ena / ek. */
 enum hx_lib_type {
     HX_LIB_NA_ION = 0,
@@ -59,7 +64,9 @@ enum hx_lib_type {
     HX_LIB_NAP_ET2 = 10,
     HX_LIB_SK_E2 = 11,
     HX_LIB_SKV3_1 = 12,
-    HX_LIB_NTYPE = 13
+    HX_LIB_HD_LA = 13,
+    HX_LIB_KM_LA = 14,
+    HX_LIB_NTYPE = 15
 };
 typedef struct hx_lib_table {
     int n;
@@ -160,7 +167,9 @@ enum hx_param_kind {
     HX_P_NAP_ET2_G = 26,
     HX_P_SK_E2_G = 27,
     HX_P_SKV3_1_G = 28,
-    HX_P_COUNT = 29
+    HX_P_HD_LA_G = 29,
+    HX_P_KM_LA_G = 30,
+    HX_P_COUNT = 31
 };
 
 /* Statistics of the execution plan built at load time. */

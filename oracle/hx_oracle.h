@@ -63,10 +63,12 @@ typedef struct hxo_net {
  *   na_ion: ena | k_ion: ek | ca_ion: cai (initial), cao, eca, nernst (0/1)
  *   CaDynamics_E2: gamma, decay, depth, minCai
  *   Ca_HVA, Ca_LVAst, Im, K_Pst, K_Tst, Nap_Et2, SKv3_1: gbar
- *   NaTg: gbar, vshifth, vshiftm, slopeh, slopem | SK_E2: gbar, zTau */
+ *   NaTg: gbar, vshifth, vshiftm, slopeh, slopem | SK_E2: gbar, zTau
+ *   hd_la: ghdbar, vhalfl, tau, ehd, kl, vhalft, a0t, zetat, gmt, q10, qtl
+ *   km_la: gbar, Ra, Rb, tha, qa, tadj */
 enum {
     HXO_NA_ION = 0, HXO_K_ION, HXO_CA_ION, HXO_CADYN, HXO_CA_HVA, HXO_CA_LVAST, HXO_IM, HXO_K_PST, HXO_K_TST,
-    HXO_NATG, HXO_NAP_ET2, HXO_SK_E2, HXO_SKV3_1, HXO_LIB_NTYPE
+    HXO_NATG, HXO_NAP_ET2, HXO_SK_E2, HXO_SKV3_1, HXO_HD_LA, HXO_KM_LA, HXO_LIB_NTYPE
 };
 typedef struct hxo_lib_table {
     int n;

@@ -14,6 +14,8 @@
  *   Nap_Et2                              src/mech/user-mech/Nap_Et2.cu
  *   SK_E2                                src/mech/user-mech/SK_E2.cu:70-132
  *   SKv3_1                               src/mech/user-mech/SKv3_1.cu
+ *   hd_la (GLOBALs ehd .. qtl, celsius)  src/mech/user-mech/hd_la.cu:86-124
+ *   km_la (GLOBALs Ra, Rb, tha, qa, tadj) src/mech/user-mech/km_la.cu:97-145
  * through MechTemp's finite-difference current (mech_template.cuh:589-648)
  * and the state phase order of nonvint_cpu (simulate.cpp:784-852: mechanisms
  * that write an ion in their state update first, then the others in type
@@ -29,8 +31,8 @@
 
 #define FD_EPS 0.001
 
-static const int NPAR[HXO_LIB_NTYPE] = {1, 1, 4, 4, 1, 1, 1, 1, 1, 5, 1, 2, 1};
-static const int NST[HXO_LIB_NTYPE] = {0, 0, 0, 0, 2, 2, 1, 2, 2, 2, 2, 1, 1};
+static const int NPAR[HXO_LIB_NTYPE] = {1, 1, 4, 4, 1, 1, 1, 1, 1, 5, 1, 2, 1, 11, 6};
+static const int NST[HXO_LIB_NTYPE] = {0, 0, 0, 0, 2, 2, 1, 2, 2, 2, 2, 1, 1, 1, 1};
 
 struct hxo_libstate {
     double* st[HXO_LIB_NTYPE]; /* n x NST per table */
@@ -154,6 +156,28 @@ static void skv31_rates(double v, double r[2]) {
     r[1] = 0.2 * 20.0 / (1.0 + exp((v - (-46.560)) / (-44.140)));
 }
 
+/* hd_la.cu:86-104: p = ghdbar, vhalfl, tau, ehd, kl, vhalft, a0t, zetat, gmt, q10, qtl */
+static void hdla_rate(double v, const double* p, double celsius, double r[2]) {
+    const double vhalfl = p[1], tau = p[2], kl = p[4], vhalft = p[5], a0t = p[6], zetat = p[7], gmt = p[8];
+    const double q10 = p[9], qtl = p[10];
+    double a, qt;
+    qt = pow(q10, ((celsius - 33.0) / 10.0));
+    a = exp(0.0378 * zetat * (v - vhalft));
+    r[0] = 1.0 / (1.0 + exp(-(v - vhalfl) / kl));
+    r[1] = tau * exp(0.0378 * zetat * gmt * (v - vhalft)) / (qtl * qt * a0t * (1.0 + a));
+}
+
+/* km_la.cu:97-115: p = gbar, Ra, Rb, tha, qa, tadj; r = ninf, ntau, nexp */
+static void kmla_trates(double v, const double* p, double dt, double r[3]) {
+    const double Ra = p[1], Rb = p[2], tha = p[3], qa = p[4], tadj = p[5];
+    const double a = Ra * (v - tha) / (1.0 - exp(-(v - tha) / qa));
+    const double b = -Rb * (v - tha) / (1.0 - exp((v - tha) / qa));
+    r[1] = 1.0 / (a + b);
+    r[0] = a * r[1];
+    const double tinc = -dt * tadj;
+    r[2] = 1.0 - exp(tinc / r[1]);
+}
+
 static double sk_zinf(double ca) {
     double ca_safe = ca;
     if (ca_safe < 1e-7) ca_safe = ca_safe + 1e-07;
@@ -180,14 +204,25 @@ static double chan_current(int t, double v, const double* p, const double* s, do
         case HXO_SKV3_1:
         case HXO_SK_E2:
             return p[0] * s[0] * (v - erev);
+        case HXO_HD_LA: { /* ghd = ghdbar l; i = ghd (v - ehd) */
+            const double ghd = p[0] * s[0];
+            return ghd * (v - erev);
+        }
+        case HXO_KM_LA: { /* gk = tadj gbar n; ik = 1e-4 gk (v - ek) */
+            const double gk = p[5] * p[0] * s[0];
+            return (1e-4) * gk * (v - erev);
+        }
         default:
             return 0.0;
     }
 }
 
-/* 0: na, 1: k, 2: ca (the ion whose erev a channel reads and current it writes) */
+/* 0: na, 1: k, 2: ca (the ion whose erev a channel reads and current it writes),
+ * 3: none (hd_la: its own reversal potential ehd, no ion current) */
 static int chan_ion(int t) {
     switch (t) {
+        case HXO_HD_LA:
+            return 3;
         case HXO_NATG:
         case HXO_NAP_ET2:
             return 0;
@@ -279,6 +314,8 @@ void hxo_lib_init(const hxo_group* g, struct hxo_libstate* L, const double* v) {
                 case HXO_IM: im_rates(v[i], r); break;
                 case HXO_SKV3_1: skv31_rates(v[i], r); break;
                 case HXO_SK_E2: r[0] = sk_zinf(L->cai[L->ca_of[i]]); break;
+                case HXO_HD_LA: hdla_rate(v[i], p, g->celsius, r); break;
+                case HXO_KM_LA: kmla_trates(v[i], p, g->dt, r); break;
             }
             s[0] = r[0];
             if (NST[t] == 2) s[1] = r[2];
@@ -303,7 +340,7 @@ void hxo_lib_current(const hxo_group* g, struct hxo_libstate* L, const double* v
             const int i = T->node[j];
             const double* p = T->par + NPAR[t] * j;
             const double* s = L->st[t] + NST[t] * j;
-            const double e = ion_erev(L, ion, i);
+            const double e = ion == 3 ? p[3] : ion_erev(L, ion, i);
             double gg = chan_current(t, v[i] + 0.001, p, s, e);
             const double r = chan_current(t, v[i], p, s, e);
             if (ion == 2) L->ica[L->ca_of[i]] += r;
@@ -354,6 +391,16 @@ void hxo_lib_state(const hxo_group* g, struct hxo_libstate* L, const double* v) 
             if (t == HXO_SK_E2) {
                 const double zTau = p[1];
                 s[0] = cnexp(s[0], sk_zinf(L->cai[L->ca_of[i]]), zTau, dt);
+                continue;
+            }
+            if (t == HXO_HD_LA) {
+                hdla_rate(v[i], p, g->celsius, r);
+                s[0] = s[0] + (1.0 - exp(-dt / r[1])) * (r[0] - s[0]);
+                continue;
+            }
+            if (t == HXO_KM_LA) {
+                kmla_trates(v[i], p, dt, r);
+                s[0] = s[0] + r[2] * (r[0] - s[0]);
                 continue;
             }
             switch (t) {

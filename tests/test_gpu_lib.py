@@ -84,34 +84,39 @@ def _fd(g, key, u, T, probes, c, h=1e-3):
     return (-vals[0] + 8 * vals[1] - 8 * vals[2] + vals[3]) / (12 * h)
 
 
-@pytest.mark.parametrize("T,h,min_resolved", [(800, 1e-3, 9), (190, 1e-2, 8)], ids=["spiking", "subthreshold"])
-def test_library_gradients_vs_finite_differences(Sim, T, h, min_resolved):
+def test_library_gradients_vs_finite_differences(Sim):
     """Spiking (800 steps: the soma fires, calcium enters) and subthreshold
-    (190 steps, before the IClamp: every voltage below -60 mV, so the
-    K_Pst time constant stays on one branch of its v < -50 switch,
-    K_Pst.cu rates) regimes; between them every kind is resolved to 1e-6."""
-    g = _group()
-    probes = _probes(g)
-    rng = np.random.default_rng(17)
-    c = rng.standard_normal((T + 1, probes.size)) * 1e-2
-    c[0] = 0.0
-    s = Sim(0)
-    s.load_group(g)
-    tr = s.forward_capture(T, probes=probes)
-    ref, _ = O.forward(g, T, probe=probes)
-    assert np.max(np.abs(tr - ref)) / np.max(np.abs(ref)) <= V_TOL
-    grads = s.backward(c, keys=LIB_KEYS)
-    resolved = 0
-    for key in LIB_KEYS:
-        mech, var = key.split(".")
-        p = g.lib[mech].fields[var]
-        u = rng.standard_normal(p.size)
-        fd = _fd(g, key, u, T, probes, c, h=h)
-        noise = abs(fd - _fd(g, key, u, T, probes, c, h=2 * h))
-        ad = float(np.sum(grads[key] * p * u))
-        assert abs(ad - fd) <= FD_TOL * abs(fd) + 4 * noise, (key, ad, fd, noise)
-        resolved += noise <= FD_TOL * abs(fd)
-    assert resolved >= min_resolved, resolved
+    (190 steps, before the IClamp: every voltage below -60 mV, so the K_Pst
+    time constant stays on one branch of its v < -50 switch, K_Pst.cu rates)
+    regimes.  Every kind must agree in both; each kind must be resolved by
+    the finite differences to 1e-4 in one of them, and all but three to 1e-6
+    (the calcium-buffer parameters gamma, depth and the Ca_HVA density move
+    the voltages least)."""
+    best = {}
+    for T, h in ((800, 1e-3), (190, 1e-2)):
+        g = _group()
+        probes = _probes(g)
+        rng = np.random.default_rng(17)
+        c = rng.standard_normal((T + 1, probes.size)) * 1e-2
+        c[0] = 0.0
+        s = Sim(0)
+        s.load_group(g)
+        tr = s.forward_capture(T, probes=probes)
+        ref, _ = O.forward(g, T, probe=probes)
+        assert np.max(np.abs(tr - ref)) / np.max(np.abs(ref)) <= V_TOL
+        grads = s.backward(c, keys=LIB_KEYS)
+        for key in LIB_KEYS:
+            mech, var = key.split(".")
+            p = g.lib[mech].fields[var]
+            u = rng.standard_normal(p.size)
+            fd = _fd(g, key, u, T, probes, c, h=h)
+            noise = abs(fd - _fd(g, key, u, T, probes, c, h=2 * h))
+            ad = float(np.sum(grads[key] * p * u))
+            assert abs(ad - fd) <= FD_TOL * abs(fd) + 4 * noise, (T, key, ad, fd, noise)
+            best[key] = min(best.get(key, np.inf), noise / abs(fd))
+        s.close()
+    assert all(r <= 1e-4 for r in best.values()), best
+    assert sum(r <= FD_TOL for r in best.values()) >= len(LIB_KEYS) - 3, best
 
 
 def test_library_checkpointed_backward_equals_full_tape(Sim):
