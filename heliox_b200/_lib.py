@@ -49,9 +49,12 @@ HX_P = {
     "SKv3_1.gSKv3_1bar": 28,
     "hd_la.ghdbar": 29,
     "km_la.gbar": 30,
+    "kca_la.gbar": 31,
+    "it2_la.gcabar": 32,
+    "kdr_la.gbar": 33,
 }
-HX_P_COUNT = 31
-HX_LIB_NTYPE = 15
+HX_P_COUNT = 34
+HX_LIB_NTYPE = 18
 
 
 class LibTable(C.Structure):

@@ -134,14 +134,15 @@ struct DevNet {
 // its fixed parameters at ent_fix[e] of fix (ions: erev / concentrations;
 // NaTg: vshifth, vshiftm, slopeh, slopem; SK_E2: zTau; hd_la: vhalfl, tau,
 // ehd, kl, vhalft, a0t, zetat, gmt and qtl q10^((celsius - 33)/10) a0t;
-// km_la: Ra, Rb, tha, qa, tadj).  Trainable
-// parameters (HX_P_CADYN_GAMMA .. HX_P_KM_LA_G) live per instance in
+// km_la: Ra, Rb, tha, qa, tadj; kca_la: Ra, Rb, caix, tadj; it2_la: vshift,
+// v12m, vwm, v12h, vwh, am, ah, vm1, vm2, vh1, vh2, wm1, wm2, wh1, wh2).  Trainable
+// parameters (HX_P_CADYN_GAMMA .. HX_P_KDR_LA_G) live per instance in
 // prm[kind - HX_P_CADYN_GAMMA], their gradients in grad[...].
-constexpr int kLibKinds = 15;
+constexpr int kLibKinds = 18;
 struct DevLib {
     int nst;
     const int *node_off, *ent, *ent_st, *ent_fix;  // node_off: nnode + 1; ent_st: nent + 1
-    const unsigned short* mask;  // per node: bit t set when the node has an entry of type t
+    const unsigned* mask;  // per node: bit t set when the node has an entry of type t
     const double* fix;
     const double* prm[kLibKinds];
     double* grad[kLibKinds];

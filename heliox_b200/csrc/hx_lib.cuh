@@ -527,6 +527,70 @@ struct KmLa {
     }
 };
 
+// kca_la.cu:100-145 (gbar in pS/um2; GLOBALs Ra, Rb, caix, tadj): the gate
+// depends on cai only; nexp = 1 - exp(-dt tadj / ntau) is the cnexp form with
+// tau = ntau / tadj.
+struct KcaLa {
+    static constexpr int kS = 1, kP = 1, kIon = 1;
+    static constexpr bool kCai = true;
+    static constexpr int kErevFix = 0;
+    template <class T>
+    __device__ static T cur(const T& v, const T* s, const T* p, const double* f, const T& e) {
+        const T gk = f[3] * p[0] * s[0];
+        return (1e-4 * gk) * (v - e);
+    }
+    template <class T>
+    __device__ static void gates(const T&, const double* f, const T& cai, T* r) {
+        const double Ra = f[0], Rb = f[1], caix = f[2], tadj = f[3];
+        const T a = Ra * pow(cai, caix);
+        const T rs = rcp(a + Rb);
+        r[0] = a * rs;
+        r[1] = rs * rcp(tadj);
+    }
+};
+
+// it2_la.cu:111-170 (T-type calcium; GLOBALs vshift .. wh2), gates at
+// v + vshift with mexp = 1 - exp(-dt / mtau).
+struct It2La {
+    static constexpr int kS = 2, kP = 1, kIon = 2;
+    static constexpr bool kCai = false;
+    static constexpr int kErevFix = 0;
+    template <class T>
+    __device__ static T cur(const T& v, const T* s, const T* p, const double*, const T& e) {
+        const T gca = p[0] * s[0] * s[0] * s[1];
+        return gca * (v - e);
+    }
+    template <class T>
+    __device__ static void gates(const T& v, const double* f, const T&, T* r) {
+        const T u = v + f[0];
+        r[0] = rcp(1.0 + exp(-(u + f[1]) * rcp(f[2])));
+        r[1] = f[5] + rcp(exp((u + f[7]) * rcp(f[11])) + exp(-(u + f[8]) * rcp(f[12])));
+        r[2] = rcp(1.0 + exp((u + f[3]) * rcp(f[4])));
+        r[3] = f[6] + rcp(exp((u + f[9]) * rcp(f[13])) + exp(-(u + f[10]) * rcp(f[14])));
+    }
+};
+
+// kdr_la.cu:67-118 (its INITIAL sets m to minf and then to 0)
+struct KdrLa {
+    static constexpr int kS = 1, kP = 1, kIon = 1;
+    static constexpr bool kCai = false;
+    static constexpr int kErevFix = 0;
+    static constexpr bool kInitZero = true;
+    template <class T>
+    __device__ static T cur(const T& v, const T* s, const T* p, const double*, const T& e) {
+        const T m2 = s[0] * s[0];
+        return p[0] * (m2 * m2) * (v - e);
+    }
+    template <class T>
+    __device__ static void gates(const T& v, const double*, const T&, T* r) {
+        r[0] = rcp(1.0 + exp((-v - 29.5) * 0.1));
+        if (val(v) < -10.0)
+            r[1] = 0.25 + 4.35 * exp((v + 10.0) * 0.1);
+        else
+            r[1] = 0.25 + 4.35 * exp((-v - 10.0) * 0.1);
+    }
+};
+
 // CaDynamics_E2.cu:101-137: cai' from cai and the step's calcium current.
 // The reference's steady term -(drive - (-minCai)/decay) / (-1/decay)
 // equals drive decay + minCai.
@@ -543,20 +607,23 @@ __device__ __forceinline__ T cadyn(const T& cai, const T& ica, const T& gamma, c
 // ------------------------------------------------------------ type table
 enum LibType : int {
     kNaIon = 0, kKIon, kCaIon, kCaDyn, kCaHVA, kCaLVAst, kIm, kKPst, kKTst, kNaTg, kNapEt2, kSKE2, kSKv31, kHdLa,
-    kKmLa, kNType
+    kKmLa, kKcaLa, kIt2La, kKdrLa, kNType
 };
+static_assert(kNType <= 32, "the per-node type mask (DevLib::mask) holds one bit per type");
 // first trainable kind of each type, relative to HX_P_CADYN_GAMMA (-1: none)
 __host__ __device__ constexpr int kind0(int t) {
     return t < kCaDyn ? -1 : t == kCaDyn ? 0 : t + 0;
 }
 // states per entry / fixed parameters per entry / trainable parameters per instance
 __host__ __device__ constexpr int nstate(int t) {
-    return t == kCaIon ? 1 : (t == kIm || t == kSKE2 || t == kSKv31 || t == kHdLa || t == kKmLa) ? 1
-                                                                                                : t >= kCaHVA ? 2 : 0;
+    return t == kCaIon ? 1
+           : (t == kIm || t == kSKE2 || t == kSKv31 || t == kHdLa || t == kKmLa || t == kKcaLa || t == kKdrLa) ? 1
+           : t >= kCaHVA ? 2
+                         : 0;
 }
 __host__ __device__ constexpr int nfix(int t) {
     return (t == kNaIon || t == kKIon) ? 1 : t == kCaIon ? 4 : t == kNaTg ? 4 : t == kSKE2 ? 1 : t == kHdLa ? 9
-                                                                                 : t == kKmLa ? 5 : 0;
+           : t == kKmLa ? 5 : t == kKcaLa ? 4 : t == kIt2La ? 15 : 0;
 }
 __host__ __device__ constexpr int ntrain(int t) { return t < kCaDyn ? 0 : t == kCaDyn ? 4 : 1; }
 
@@ -571,7 +638,10 @@ __host__ __device__ constexpr int ntrain(int t) { return t < kCaDyn ? 0 : t == k
     X(kSKE2, SKE2)         \
     X(kSKv31, SKv31)       \
     X(kHdLa, HdLa)         \
-    X(kKmLa, KmLa)
+    X(kKmLa, KmLa)         \
+    X(kKcaLa, KcaLa)       \
+    X(kIt2La, It2La)       \
+    X(kKdrLa, KdrLa)
 
 // ------------------------------------------------------------ drivers
 // one channel's forward contribution; returns I(v) (the ion current)
@@ -622,13 +692,21 @@ __device__ __forceinline__ void chan_state(double v, double dt, double* s, const
     for (int j = 0; j < M::kS; ++j) s[j] = cnexp(s[j], r[2 * j], r[2 * j + 1], dt);
 }
 
-// INITIAL: every gate at its steady state
+// INITIAL: every gate at its steady state (kdr_la: at 0)
+template <class M, class = void>
+struct InitZero {
+    static constexpr bool value = false;
+};
+template <class M>
+struct InitZero<M, decltype((void)M::kInitZero)> {
+    static constexpr bool value = M::kInitZero;
+};
 template <class M>
 __device__ __forceinline__ void chan_init(double v, double* s, const double* f, double cai) {
     double r[2 * M::kS];
     M::template gates<double>(v, f, cai, r);
 #pragma unroll
-    for (int j = 0; j < M::kS; ++j) s[j] = r[2 * j];
+    for (int j = 0; j < M::kS; ++j) s[j] = InitZero<M>::value ? 0.0 : r[2 * j];
 }
 
 // Adjoint of one channel's state update s_{k+1} = F(v_{k+1}, s_k[, cai_{k+1}]):

@@ -84,6 +84,10 @@ LIB_MECHS = (
     ("SKv3_1", ("gSKv3_1bar",), 1),
     ("hd_la", ("ghdbar", "vhalfl", "tau", "ehd", "kl", "vhalft", "a0t", "zetat", "gmt", "q10", "qtl"), 1),
     ("km_la", ("gbar", "Ra", "Rb", "tha", "qa", "tadj"), 1),
+    ("kca_la", ("gbar", "Ra", "Rb", "caix", "tadj"), 1),
+    ("it2_la", ("gcabar", "vshift", "v12m", "vwm", "v12h", "vwh", "am", "ah", "vm1", "vm2", "vh1", "vh2", "wm1",
+                "wm2", "wh1", "wh2"), 1),
+    ("kdr_la", ("gbar",), 1),
 )
 # fields that are GLOBALs of their mechanism in the reference (one value per
 # group, written to globals.dat as <field>_<mechanism>)
@@ -91,6 +95,9 @@ LIB_GLOBALS = {
     "SK_E2": ("zTau",),
     "hd_la": ("ehd", "kl", "vhalft", "a0t", "zetat", "gmt", "q10", "qtl"),
     "km_la": ("Ra", "Rb", "tha", "qa", "tadj"),
+    "kca_la": ("Ra", "Rb", "caix", "tadj"),
+    "it2_la": ("vshift", "v12m", "vwm", "v12h", "vwh", "am", "ah", "vm1", "vm2", "vh1", "vh2", "wm1", "wm2", "wh1",
+               "wh2"),
 }
 LIB_NAMES = tuple(m[0] for m in LIB_MECHS)
 LIB_FIELDS = {m[0]: m[1] for m in LIB_MECHS}
@@ -99,7 +106,7 @@ LIB_NTRAIN = {m[0]: m[2] for m in LIB_MECHS}
 LIB_IONS = {
     "CaDynamics_E2": ("ca",), "Ca_HVA": ("ca",), "Ca_LVAst": ("ca",), "Im": ("k",), "K_Pst": ("k",),
     "K_Tst": ("k",), "NaTg": ("na",), "Nap_Et2": ("na",), "SK_E2": ("k", "ca"), "SKv3_1": ("k",),
-    "hd_la": (), "km_la": ("k",),
+    "hd_la": (), "km_la": ("k",), "kca_la": ("k", "ca"), "it2_la": ("ca",), "kdr_la": ("k",),
 }
 
 
@@ -373,7 +380,7 @@ def lib_par_matrix(g: "CellGroup", name: str) -> np.ndarray:
 # states per library table, in the order the forward keeps them
 LIB_STATES = {"ca_ion": ("cai",), "Ca_HVA": ("m", "h"), "Ca_LVAst": ("m", "h"), "Im": ("m",), "K_Pst": ("m", "h"),
               "K_Tst": ("m", "h"), "NaTg": ("m", "h"), "Nap_Et2": ("m", "h"), "SK_E2": ("z",), "SKv3_1": ("m",),
-              "hd_la": ("l",), "km_la": ("n",)}
+              "hd_la": ("l",), "km_la": ("n",), "kca_la": ("n",), "it2_la": ("m", "h"), "kdr_la": ("m",)}
 
 
 def empty_table(names, inames=()) -> MechTable:

@@ -16,6 +16,9 @@
  *   SKv3_1                               src/mech/user-mech/SKv3_1.cu
  *   hd_la (GLOBALs ehd .. qtl, celsius)  src/mech/user-mech/hd_la.cu:86-124
  *   km_la (GLOBALs Ra, Rb, tha, qa, tadj) src/mech/user-mech/km_la.cu:97-145
+ *   kca_la (GLOBALs Ra, Rb, caix, tadj)  src/mech/user-mech/kca_la.cu:100-145
+ *   it2_la (GLOBALs vshift .. wh2)       src/mech/user-mech/it2_la.cu:111-170
+ *   kdr_la                               src/mech/user-mech/kdr_la.cu:67-118
  * through MechTemp's finite-difference current (mech_template.cuh:589-648)
  * and the state phase order of nonvint_cpu (simulate.cpp:784-852: mechanisms
  * that write an ion in their state update first, then the others in type
@@ -31,8 +34,8 @@
 
 #define FD_EPS 0.001
 
-static const int NPAR[HXO_LIB_NTYPE] = {1, 1, 4, 4, 1, 1, 1, 1, 1, 5, 1, 2, 1, 11, 6};
-static const int NST[HXO_LIB_NTYPE] = {0, 0, 0, 0, 2, 2, 1, 2, 2, 2, 2, 1, 1, 1, 1};
+static const int NPAR[HXO_LIB_NTYPE] = {1, 1, 4, 4, 1, 1, 1, 1, 1, 5, 1, 2, 1, 11, 6, 5, 16, 1};
+static const int NST[HXO_LIB_NTYPE] = {0, 0, 0, 0, 2, 2, 1, 2, 2, 2, 2, 1, 1, 1, 1, 1, 2, 1};
 
 struct hxo_libstate {
     double* st[HXO_LIB_NTYPE]; /* n x NST per table */
@@ -178,6 +181,41 @@ static void kmla_trates(double v, const double* p, double dt, double r[3]) {
     r[2] = 1.0 - exp(tinc / r[1]);
 }
 
+/* kca_la.cu:100-110: p = gbar, Ra, Rb, caix, tadj; r = ninf, ntau, nexp */
+static void kcala_rates(double cai, const double* p, double dt, double r[3]) {
+    const double Ra = p[1], Rb = p[2], caix = p[3], tadj = p[4];
+    const double a = Ra * pow(cai, caix);
+    const double b = Rb;
+    r[1] = 1.0 / (a + b);
+    r[0] = a * r[1];
+    const double tinc = -dt * tadj;
+    r[2] = 1.0 - exp(tinc / r[1]);
+}
+
+/* it2_la.cu:111-130 at v_ = v + vshift: r = minf, mexp, hinf, hexp */
+static void it2la_trates(double v_, const double* p, double dt, double r[4]) {
+    const double v12m = p[2], vwm = p[3], v12h = p[4], vwh = p[5], am = p[6], ah = p[7], vm1 = p[8], vm2 = p[9];
+    const double vh1 = p[10], vh2 = p[11], wm1 = p[12], wm2 = p[13], wh1 = p[14], wh2 = p[15];
+    const double minf = 1.0 / (1.0 + exp(-(v_ + v12m) / vwm));
+    const double hinf = 1.0 / (1.0 + exp((v_ + v12h) / vwh));
+    const double mtau = (am + 1.0 / (exp((v_ + vm1) / wm1) + exp(-(v_ + vm2) / wm2)));
+    const double htau = (ah + 1.0 / (exp((v_ + vh1) / wh1) + exp(-(v_ + vh2) / wh2)));
+    const double tinc = -dt;
+    r[0] = minf;
+    r[1] = 1.0 - exp(tinc / mtau);
+    r[2] = hinf;
+    r[3] = 1.0 - exp(tinc / htau);
+}
+
+/* kdr_la.cu:67-77 (settables): r = minf, mtau */
+static void kdrla_settables(double v, double r[2]) {
+    r[0] = 1.0 / (1.0 + exp((-v - 29.5) / 10.0));
+    if (v < -10.0)
+        r[1] = 0.25 + 4.35 * exp((v + 10.0) / 10.0);
+    else
+        r[1] = 0.25 + 4.35 * exp((-v - 10.0) / 10.0);
+}
+
 static double sk_zinf(double ca) {
     double ca_safe = ca;
     if (ca_safe < 1e-7) ca_safe = ca_safe + 1e-07;
@@ -212,6 +250,18 @@ static double chan_current(int t, double v, const double* p, const double* s, do
             const double gk = p[5] * p[0] * s[0];
             return (1e-4) * gk * (v - erev);
         }
+        case HXO_KCA_LA: {
+            const double gk = p[4] * p[0] * s[0];
+            return (1e-4) * gk * (v - erev);
+        }
+        case HXO_IT2_LA: {
+            const double gca = p[0] * s[0] * s[0] * s[1];
+            return gca * (v - erev);
+        }
+        case HXO_KDR_LA: {
+            const double m_4 = s[0] * s[0] * s[0] * s[0];
+            return p[0] * m_4 * (v - erev);
+        }
         default:
             return 0.0;
     }
@@ -228,6 +278,7 @@ static int chan_ion(int t) {
             return 0;
         case HXO_CA_HVA:
         case HXO_CA_LVAST:
+        case HXO_IT2_LA:
             return 2;
         default:
             return 1;
@@ -316,6 +367,9 @@ void hxo_lib_init(const hxo_group* g, struct hxo_libstate* L, const double* v) {
                 case HXO_SK_E2: r[0] = sk_zinf(L->cai[L->ca_of[i]]); break;
                 case HXO_HD_LA: hdla_rate(v[i], p, g->celsius, r); break;
                 case HXO_KM_LA: kmla_trates(v[i], p, g->dt, r); break;
+                case HXO_KCA_LA: kcala_rates(L->cai[L->ca_of[i]], p, g->dt, r); break;
+                case HXO_IT2_LA: it2la_trates(v[i] + p[1], p, g->dt, r); break;
+                case HXO_KDR_LA: kdrla_settables(v[i], r); r[0] = 0.0; break; /* m = minf; m = 0.0 */
             }
             s[0] = r[0];
             if (NST[t] == 2) s[1] = r[2];
@@ -401,6 +455,22 @@ void hxo_lib_state(const hxo_group* g, struct hxo_libstate* L, const double* v) 
             if (t == HXO_KM_LA) {
                 kmla_trates(v[i], p, dt, r);
                 s[0] = s[0] + r[2] * (r[0] - s[0]);
+                continue;
+            }
+            if (t == HXO_KCA_LA) {
+                kcala_rates(L->cai[L->ca_of[i]], p, dt, r);
+                s[0] = s[0] + r[2] * (r[0] - s[0]);
+                continue;
+            }
+            if (t == HXO_IT2_LA) {
+                it2la_trates(v[i] + p[1], p, dt, r);
+                s[0] = s[0] + r[1] * (r[0] - s[0]);
+                s[1] = s[1] + r[3] * (r[2] - s[1]);
+                continue;
+            }
+            if (t == HXO_KDR_LA) {
+                kdrla_settables(v[i], r);
+                s[0] = s[0] + (1.0 - exp(-dt / r[1])) * (r[0] - s[0]);
                 continue;
             }
             switch (t) {
