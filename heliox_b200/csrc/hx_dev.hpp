@@ -131,7 +131,8 @@ struct DevNet {
 // CoreNEURON type order (ions, CaDynamics_E2, channels): entry e has code
 // type << 24 | instance (GPU instance order of its type), its states at
 // ent_st[e] of the flat state array (ca_ion: cai; channels: their gates) and
-// its fixed parameters at ent_fix[e] of fix (ions: erev / concentrations;
+// its fixed parameters at ent_fix[e] of fix (entries of a type with equal
+// values share one copy) (ions: erev / concentrations;
 // NaTg: vshifth, vshiftm, slopeh, slopem; SK_E2: zTau; hd_la: vhalfl, tau,
 // ehd, kl, vhalft, a0t, zetat, gmt and qtl q10^((celsius - 33)/10) a0t;
 // km_la: Ra, Rb, tha, qa, tadj; kca_la: Ra, Rb, caix, tadj; it2_la: vshift,

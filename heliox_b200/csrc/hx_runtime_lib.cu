@@ -10,6 +10,7 @@
 // owns the node walks them in the order the reference's type loop applies
 // them.
 #include <cmath>
+#include <map>
 #include <string>
 #include <vector>
 
@@ -126,6 +127,7 @@ int hx_lib_load(hx_ctx* ctx, const hx_group_desc* desc) {
     std::vector<int> node_off(nn + 1, 0), ent, ent_st, ent_fix;
     std::vector<unsigned> mask(std::max(nn, 1), 0);
     std::vector<double> fix;
+    std::vector<std::map<std::vector<double>, int>> fix_of(HX_LIB_NTYPE);
     std::vector<int> inst(HX_LIB_NTYPE, 0);
     std::vector<std::vector<double>> prm(hx::kLibKinds);
     for (int k = 0; k < hx::kLibKinds; k++) prm[k].assign(1, 0.0);
@@ -143,16 +145,24 @@ int hx_lib_load(hx_ctx* ctx, const hx_group_desc* desc) {
             mask[gi] |= 1u << t;
             ent_st.push_back(nst);
             nst += L::nstate(t);
-            ent_fix.push_back((int)fix.size());
+            std::vector<double> fv;
             if (t == HX_LIB_HD_LA) {
                 // vhalfl, tau, ehd, kl, vhalft, a0t, zetat, gmt, then qtl * qt * a0t with
                 // qt = pow(q10, (celsius - 33) / 10) as hd_la.cu:94 computes it
-                for (int c = 1; c <= 8; c++) fix.push_back(par[c]);
+                for (int c = 1; c <= 8; c++) fv.push_back(par[c]);
                 const double qt = std::pow(par[9], ((desc->celsius - 33.0) / 10.0));
-                fix.push_back(par[10] * qt * par[6]);
+                fv.push_back(par[10] * qt * par[6]);
             } else {
-                for (int c = 0; c < nfx; c++) fix.push_back(par[ntr + c]);
+                for (int c = 0; c < nfx; c++) fv.push_back(par[ntr + c]);
             }
+            // entries with equal fixed parameters (GLOBALs, shared ion constants)
+            // share one copy, so that their reads stay in cache
+            auto it = fix_of[t].find(fv);
+            if (it == fix_of[t].end()) {
+                it = fix_of[t].emplace(fv, (int)fix.size()).first;
+                fix.insert(fix.end(), fv.begin(), fv.end());
+            }
+            ent_fix.push_back(it->second);
             const int k0 = L::kind0(t);
             for (int c = 0; c < ntr; c++) {
                 std::vector<double>& pv = prm[k0 + c];
