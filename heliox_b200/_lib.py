@@ -52,9 +52,11 @@ HX_P = {
     "kca_la.gbar": 31,
     "it2_la.gcabar": 32,
     "kdr_la.gbar": 33,
+    "sca_la.gbar": 34,
+    "Ca.gCabar": 35,
 }
-HX_P_COUNT = 34
-HX_LIB_NTYPE = 18
+HX_P_COUNT = 36
+HX_LIB_NTYPE = 20
 
 
 class LibTable(C.Structure):

@@ -76,6 +76,8 @@ LIB_MECH_TABLE: List[Tuple[int, str, int, int, int, int, int, float]] = [
     (28, "kca_la", 0, 0, 0, 14, 0, 0.0),
     (29, "it2_la", 0, 0, 0, 16, 0, 0.0),
     (30, "kdr_la", 0, 0, 0, 8, 0, 0.0),
+    (31, "sca_la", 0, 0, 0, 18, 0, 0.0),
+    (32, "Ca", 0, 0, 0, 14, 0, 0.0),
 ]
 # data column of each library field (its var_in_coredata_idx); SK_E2.zTau is
 # the GLOBAL zTau_SK_E2 of globals.dat (SK_E2.cu:65-66)
@@ -86,13 +88,16 @@ LIB_COLUMNS = {
     "NaTg": {"gNaTgbar": 0, "vshifth": 1, "vshiftm": 2, "slopeh": 3, "slopem": 4},
     "Nap_Et2": {"gNap_Et2bar": 0}, "SK_E2": {"gSK_E2bar": 0}, "SKv3_1": {"gSKv3_1bar": 0},
     "hd_la": {"ghdbar": 0, "vhalfl": 1, "tau": 2}, "km_la": {"gbar": 0}, "kca_la": {"gbar": 0},
-    "it2_la": {"gcabar": 0}, "kdr_la": {"gbar": 0},
+    "it2_la": {"gcabar": 0}, "kdr_la": {"gbar": 0}, "sca_la": {"inactF": 0, "actF": 1, "gbar": 2},
+    "Ca": {"gCabar": 0},
 }
 # GLOBALs the loader requires of a mechanism that the dynamics do not read
 # (km_la.cu:70-80: its table parameters), written with these values
 LIB_EXTRA_GLOBALS = {"km_la": {"temp": 23.0, "q10": 2.3, "vmin": -120.0, "vmax": 100.0, "usetable": 0.0},
                      "kca_la": {"q10": 2.3, "temp": 23.0, "vmin": -120.0, "vmax": 100.0},
-                     "it2_la": {"vmin": -120.0, "vmax": 100.0, "cao": 2.0, "cai": 2.4e-4}}
+                     "it2_la": {"vmin": -120.0, "vmax": 100.0, "cao": 2.0, "cai": 2.4e-4},
+                     "sca_la": {"temp": 23.0, "q10": 2.3, "vmin": -120.0, "vmax": 100.0, "cao": 2.5, "cai": 1e-4,
+                                "usetable": 0.0}}
 # ca_ion iontype with Nernst reversal potentials at finitialize and every step
 # (eion.cuh:165, 181: bits 040 and 0100)
 IONTYPE_NERNST = 0o140

@@ -591,6 +591,65 @@ struct KdrLa {
     }
 };
 
+// sca_la.cu:95-160 (gbar in pS/um2; RANGE inactF, actF; GLOBALs vshift,
+// tadj): gates at v + vshift, mexp = 1 - exp(-dt tadj / mtau) (the cnexp
+// form with tau = mtau / tadj).
+struct ScaLa {
+    static constexpr int kS = 2, kP = 1, kIon = 2;
+    static constexpr bool kCai = false;
+    static constexpr int kErevFix = 0;
+    template <class T>
+    __device__ static T cur(const T& v, const T* s, const T* p, const double* f, const T& e) {
+        const T gca = f[3] * p[0] * s[0] * s[0] * s[1];
+        return (1e-4 * gca) * (v - e);
+    }
+    template <class T>
+    __device__ static void gates(const T& v, const double* f, const T&, T* r) {
+        const double ia = rcp(f[1]), ii = rcp(f[0]), it = rcp(f[3]);
+        const T vm = v + f[2];
+        const T x = -27.0 - vm;
+        const T a = (0.055 * x) * rcp(exp(x * (1.0 / 3.8)) - 1.0) * ia;
+        const T b = (0.94 * exp((-75.0 - vm) * (1.0 / 17.0))) * ia;
+        const T rm = rcp(a + b);
+        r[0] = a * rm;
+        r[1] = rm * it;
+        const T a2 = (0.000457 * exp((-13.0 - vm) * 0.02)) * ii;
+        const T b2 = (0.0065 * rcp(exp((-vm - 15.0) * (1.0 / 28.0)) + 1.0)) * ii;
+        const T rh = rcp(a2 + b2);
+        r[2] = a2 * rh;
+        r[3] = rh * it;
+    }
+};
+
+// Ca.cu (the high-voltage calcium current without CA_HVA's vtrap: v = -27
+// is moved by 1e-4)
+struct CaPlain {
+    static constexpr int kS = 2, kP = 1, kIon = 2;
+    static constexpr bool kCai = false;
+    static constexpr int kErevFix = 0;
+    template <class T>
+    __device__ static T cur(const T& v, const T* s, const T* p, const double*, const T& e) {
+        const T g = p[0] * s[0] * s[0] * s[1];
+        return g * (v - e);
+    }
+    template <class T>
+    __device__ static void gates(const T& v0, const double*, const T&, T* r) {
+        T v = v0;
+        if (val(v) == -27.0) v = v + 0.0001;
+        const T x = -27.0 - v;
+        const T mA = (0.055 * x) * rcp(exp(x * (1.0 / 3.8)) - 1.0);
+        const T mB = 0.94 * exp((-75.0 - v) * (1.0 / 17.0));
+        const T rm = rcp(mA + mB);
+        r[0] = mA * rm;
+        r[1] = rm;
+        const T hA = 0.000457 * exp((-13.0 - v) * 0.02);
+        const T hB = 0.0065 * rcp(exp((-v - 15.0) * (1.0 / 28.0)) + 1.0);
+        const T rh = rcp(hA + hB);
+        r[2] = hA * rh;
+        r[3] = rh;
+    }
+};
+
 // CaDynamics_E2.cu:101-137: cai' from cai and the step's calcium current.
 // The reference's steady term -(drive - (-minCai)/decay) / (-1/decay)
 // equals drive decay + minCai.
@@ -607,7 +666,7 @@ __device__ __forceinline__ T cadyn(const T& cai, const T& ica, const T& gamma, c
 // ------------------------------------------------------------ type table
 enum LibType : int {
     kNaIon = 0, kKIon, kCaIon, kCaDyn, kCaHVA, kCaLVAst, kIm, kKPst, kKTst, kNaTg, kNapEt2, kSKE2, kSKv31, kHdLa,
-    kKmLa, kKcaLa, kIt2La, kKdrLa, kNType
+    kKmLa, kKcaLa, kIt2La, kKdrLa, kScaLa, kCaPlain, kNType
 };
 static_assert(kNType <= 32, "the per-node type mask (DevLib::mask) holds one bit per type");
 // first trainable kind of each type, relative to HX_P_CADYN_GAMMA (-1: none)
@@ -623,7 +682,7 @@ __host__ __device__ constexpr int nstate(int t) {
 }
 __host__ __device__ constexpr int nfix(int t) {
     return (t == kNaIon || t == kKIon) ? 1 : t == kCaIon ? 4 : t == kNaTg ? 4 : t == kSKE2 ? 1 : t == kHdLa ? 9
-           : t == kKmLa ? 5 : t == kKcaLa ? 4 : t == kIt2La ? 15 : 0;
+           : t == kKmLa ? 5 : t == kKcaLa ? 4 : t == kIt2La ? 15 : t == kScaLa ? 4 : 0;
 }
 __host__ __device__ constexpr int ntrain(int t) { return t < kCaDyn ? 0 : t == kCaDyn ? 4 : 1; }
 
@@ -641,7 +700,9 @@ __host__ __device__ constexpr int ntrain(int t) { return t < kCaDyn ? 0 : t == k
     X(kKmLa, KmLa)         \
     X(kKcaLa, KcaLa)       \
     X(kIt2La, It2La)       \
-    X(kKdrLa, KdrLa)
+    X(kKdrLa, KdrLa)       \
+    X(kScaLa, ScaLa)       \
+    X(kCaPlain, CaPlain)
 
 // ------------------------------------------------------------ drivers
 // one channel's forward contribution; returns I(v) (the ion current)

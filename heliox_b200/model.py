@@ -88,6 +88,8 @@ LIB_MECHS = (
     ("it2_la", ("gcabar", "vshift", "v12m", "vwm", "v12h", "vwh", "am", "ah", "vm1", "vm2", "vh1", "vh2", "wm1",
                 "wm2", "wh1", "wh2"), 1),
     ("kdr_la", ("gbar",), 1),
+    ("sca_la", ("gbar", "inactF", "actF", "vshift", "tadj"), 1),
+    ("Ca", ("gCabar",), 1),
 )
 # fields that are GLOBALs of their mechanism in the reference (one value per
 # group, written to globals.dat as <field>_<mechanism>)
@@ -98,6 +100,7 @@ LIB_GLOBALS = {
     "kca_la": ("Ra", "Rb", "caix", "tadj"),
     "it2_la": ("vshift", "v12m", "vwm", "v12h", "vwh", "am", "ah", "vm1", "vm2", "vh1", "vh2", "wm1", "wm2", "wh1",
                "wh2"),
+    "sca_la": ("vshift", "tadj"),
 }
 LIB_NAMES = tuple(m[0] for m in LIB_MECHS)
 LIB_FIELDS = {m[0]: m[1] for m in LIB_MECHS}
@@ -106,7 +109,8 @@ LIB_NTRAIN = {m[0]: m[2] for m in LIB_MECHS}
 LIB_IONS = {
     "CaDynamics_E2": ("ca",), "Ca_HVA": ("ca",), "Ca_LVAst": ("ca",), "Im": ("k",), "K_Pst": ("k",),
     "K_Tst": ("k",), "NaTg": ("na",), "Nap_Et2": ("na",), "SK_E2": ("k", "ca"), "SKv3_1": ("k",),
-    "hd_la": (), "km_la": ("k",), "kca_la": ("k", "ca"), "it2_la": ("ca",), "kdr_la": ("k",),
+    "hd_la": (), "km_la": ("k",), "kca_la": ("k", "ca"), "it2_la": ("ca",), "kdr_la": ("k",), "sca_la": ("ca",),
+    "Ca": ("ca",),
 }
 
 
@@ -380,7 +384,8 @@ def lib_par_matrix(g: "CellGroup", name: str) -> np.ndarray:
 # states per library table, in the order the forward keeps them
 LIB_STATES = {"ca_ion": ("cai",), "Ca_HVA": ("m", "h"), "Ca_LVAst": ("m", "h"), "Im": ("m",), "K_Pst": ("m", "h"),
               "K_Tst": ("m", "h"), "NaTg": ("m", "h"), "Nap_Et2": ("m", "h"), "SK_E2": ("z",), "SKv3_1": ("m",),
-              "hd_la": ("l",), "km_la": ("n",), "kca_la": ("n",), "it2_la": ("m", "h"), "kdr_la": ("m",)}
+              "hd_la": ("l",), "km_la": ("n",), "kca_la": ("n",), "it2_la": ("m", "h"), "kdr_la": ("m",),
+              "sca_la": ("m", "h"), "Ca": ("m", "h")}
 
 
 def empty_table(names, inames=()) -> MechTable:

@@ -246,6 +246,8 @@ LIB_DENSITY = {
     "kca_la": (5.0, 0.0, 1.0),  # pS/um^2
     "it2_la": (0.0, 0.0, 2e-4),
     "kdr_la": (0.0, 0.01, 0.0),
+    "sca_la": (0.0, 0.0, 0.5),  # pS/um^2
+    "Ca": (2e-4, 0.0, 0.0),
 }
 # GLOBALs of hd_la / km_la (one value per group; their published defaults,
 # km_la's tadj = 2.3^((34 - 23) / 10)) and hd_la's per-instance vhalfl, tau
@@ -255,6 +257,7 @@ LIB_LA_GLOBALS = {
     "kca_la": dict(Ra=0.01, Rb=0.02, caix=1.0, tadj=2.3 ** 1.1),
     "it2_la": dict(vshift=0.0, v12m=50.0, vwm=7.4, v12h=78.0, vwh=5.0, am=3.0, ah=85.0, vm1=25.0, vm2=100.0,
                    vh1=46.0, vh2=405.0, wm1=20.0, wm2=15.0, wh1=4.0, wh2=50.0),
+    "sca_la": dict(vshift=0.0, tadj=2.3 ** 1.1),
 }
 LIB_CADYN = (dict(gamma=5e-4, decay=460.0), dict(gamma=5e-4, decay=100.0), dict(gamma=5e-4, decay=80.0))
 LIB_GBAR_FIELD = {nm: LIB_FIELDS[nm][0] for nm in LIB_DENSITY}
@@ -267,7 +270,7 @@ def lib_tree_cell(seed: int, ncomp: int | None = None, nmin: int = 100, nmax: in
     The morphology is ``random_tree_cell``'s (soma, a 4-compartment axon
     initial segment, tapering dendrites).  Every compartment gets pas
     (g 3e-5, e -75); the channels of ``LIB_DENSITY`` (the user-mech set and
-    hd_la, km_la, kca_la, it2_la, kdr_la, with the GLOBALs of
+    hd_la, km_la, kca_la, it2_la, kdr_la, sca_la, Ca, with the GLOBALs of
     ``LIB_LA_GLOBALS``) go where their region's density is nonzero, scaled
     by a seeded lognormal factor (sigma 0.1);
     CaDynamics_E2 sits with the Ca channels (depth 0.1 um, minCai 1e-4 mM);
@@ -296,6 +299,8 @@ def lib_tree_cell(seed: int, ncomp: int | None = None, nmin: int = 100, nmax: in
             f["zTau"] = _f64(np.ones(nodes.size))
         if nm == "hd_la":
             f.update(vhalfl=_f64(np.full(nodes.size, -81.0)), tau=_f64(np.ones(nodes.size)))
+        if nm == "sca_la":
+            f.update(inactF=_f64(np.full(nodes.size, 3.0)), actF=_f64(np.ones(nodes.size)))
         for k, val in LIB_LA_GLOBALS.get(nm, {}).items():
             f[k] = _f64(np.full(nodes.size, val))
         lib[nm] = MechTable(_i32(nodes), f)

@@ -32,7 +32,7 @@ typedef struct hx_ctx hx_ctx;
 /* Library mechanisms: the ions and the user-mech channel set, CoreNEURON
  * types after the network mechanisms in this order (src/mech/eion.cuh,
  * src/mech/user-mech/{CaDynamics_E2,CA_HVA,Ca_LVAst,Im,K_Pst,K_Tst,NaTg,
- * Nap_Et2,SK_E2,SKv3_1,hd_la,km_la,kca_la,it2_la,kdr_la}.cu through MechTemp, src/mech/mech_template.cuh:
+ * Nap_Et2,SK_E2,SKv3_1,hd_la,km_la,kca_la,it2_la,kdr_la,sca_la,Ca}.cu through MechTemp, src/mech/mech_template.cuh:
  * 589-767).  Each table holds n instances on sorted, distinct reference nodes;
  * par holds the type's columns instance by instance (row-major):
  *   HX_LIB_NA_ION: ena | HX_LIB_K_ION: ek
@@ -51,9 +51,12 @@ typedef struct hx_ctx hx_ctx;
  *   HX_LIB_IT2_LA (it2_la.cu): gcabar, then its GLOBALs vshift, v12m, vwm,
  *                  v12h, vwh, am, ah, vm1, vm2, vh1, vh2, wm1, wm2, wh1, wh2
  *   HX_LIB_KDR_LA (kdr_la.cu): gbar
+ *   HX_LIB_SCA_LA (sca_la.cu): gbar (pS/um2), inactF, actF, then its GLOBALs
+ *                  vshift, tadj
+ *   HX_LIB_CA (Ca.cu): gCabar
  * A channel needs its ion on its node (Na: NaTg, Nap_Et2; K: Im, K_Pst,
  * K_Tst, SK_E2, SKv3_1, km_la, kca_la, kdr_la; Ca: CaDynamics_E2, Ca_HVA,
- * Ca_LVAst, it2_la, SK_E2 and kca_la (cai)); hd_la's current is nonspecific
+ * Ca_LVAst, it2_la, sca_la, Ca, SK_E2 and kca_la (cai)); hd_la's current is nonspecific
  * (its own ehd);
  * na_ion / k_ion on an hh node carry hh's ena / ek. */
 enum hx_lib_type {
@@ -75,7 +78,9 @@ enum hx_lib_type {
     HX_LIB_KCA_LA = 15,
     HX_LIB_IT2_LA = 16,
     HX_LIB_KDR_LA = 17,
-    HX_LIB_NTYPE = 18
+    HX_LIB_SCA_LA = 18,
+    HX_LIB_CA = 19,
+    HX_LIB_NTYPE = 20
 };
 typedef struct hx_lib_table {
     int n;
@@ -181,7 +186,9 @@ enum hx_param_kind {
     HX_P_KCA_LA_G = 31,
     HX_P_IT2_LA_G = 32,
     HX_P_KDR_LA_G = 33,
-    HX_P_COUNT = 34
+    HX_P_SCA_LA_G = 34,
+    HX_P_CA_G = 35,
+    HX_P_COUNT = 36
 };
 
 /* Statistics of the execution plan built at load time. */

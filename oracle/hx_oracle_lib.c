@@ -19,6 +19,8 @@
  *   kca_la (GLOBALs Ra, Rb, caix, tadj)  src/mech/user-mech/kca_la.cu:100-145
  *   it2_la (GLOBALs vshift .. wh2)       src/mech/user-mech/it2_la.cu:111-170
  *   kdr_la                               src/mech/user-mech/kdr_la.cu:67-118
+ *   sca_la (GLOBALs vshift, tadj)        src/mech/user-mech/sca_la.cu:95-160
+ *   Ca                                   src/mech/user-mech/Ca.cu
  * through MechTemp's finite-difference current (mech_template.cuh:589-648)
  * and the state phase order of nonvint_cpu (simulate.cpp:784-852: mechanisms
  * that write an ion in their state update first, then the others in type
@@ -34,8 +36,8 @@
 
 #define FD_EPS 0.001
 
-static const int NPAR[HXO_LIB_NTYPE] = {1, 1, 4, 4, 1, 1, 1, 1, 1, 5, 1, 2, 1, 11, 6, 5, 16, 1};
-static const int NST[HXO_LIB_NTYPE] = {0, 0, 0, 0, 2, 2, 1, 2, 2, 2, 2, 1, 1, 1, 1, 1, 2, 1};
+static const int NPAR[HXO_LIB_NTYPE] = {1, 1, 4, 4, 1, 1, 1, 1, 1, 5, 1, 2, 1, 11, 6, 5, 16, 1, 5, 1};
+static const int NST[HXO_LIB_NTYPE] = {0, 0, 0, 0, 2, 2, 1, 2, 2, 2, 2, 1, 1, 1, 1, 1, 2, 1, 2, 2};
 
 struct hxo_libstate {
     double* st[HXO_LIB_NTYPE]; /* n x NST per table */
@@ -216,6 +218,39 @@ static void kdrla_settables(double v, double r[2]) {
         r[1] = 0.25 + 4.35 * exp((-v - 10.0) / 10.0);
 }
 
+/* sca_la.cu:95-125 at vm = v + vshift: p = gbar, inactF, actF, vshift, tadj;
+ * r = minf, mexp, hinf, hexp */
+static void scala_trates(double vm, const double* p, double dt, double r[4]) {
+    const double inactF = p[1], actF = p[2], tadj = p[4];
+    double a, b;
+    a = 0.055 * (-27.0 - vm) / (exp((-27.0 - vm) / 3.8) - 1.0) / actF;
+    b = 0.94 * exp((-75.0 - vm) / 17.0) / actF;
+    const double mtau = 1.0 / (a + b);
+    const double minf = a * mtau;
+    a = 0.000457 * exp((-13.0 - vm) / 50.0) / inactF;
+    b = 0.0065 / (exp((-vm - 15.0) / 28.0) + 1.0) / inactF;
+    const double htau = 1.0 / (a + b);
+    const double hinf = a * htau;
+    const double tinc = -dt * tadj;
+    r[0] = minf;
+    r[1] = 1.0 - exp(tinc / mtau);
+    r[2] = hinf;
+    r[3] = 1.0 - exp(tinc / htau);
+}
+
+/* Ca.cu rates (volt == -27 moved by 1e-4); r = mInf, mTau, hInf, hTau */
+static void ca_rates(double volt, double r[4]) {
+    if (volt == -27.0) volt = volt + 0.0001;
+    const double mA = (0.055 * (-27.0 - volt)) / (exp((-27.0 - volt) / 3.8) - 1.0);
+    const double mB = (0.94 * exp((-75.0 - volt) / 17.0));
+    r[0] = mA / (mA + mB);
+    r[1] = 1.0 / (mA + mB);
+    const double hA = (0.000457 * exp((-13.0 - volt) / 50.0));
+    const double hB = (0.0065 / (exp((-volt - 15.0) / 28.0) + 1.0));
+    r[2] = hA / (hA + hB);
+    r[3] = 1.0 / (hA + hB);
+}
+
 static double sk_zinf(double ca) {
     double ca_safe = ca;
     if (ca_safe < 1e-7) ca_safe = ca_safe + 1e-07;
@@ -262,6 +297,14 @@ static double chan_current(int t, double v, const double* p, const double* s, do
             const double m_4 = s[0] * s[0] * s[0] * s[0];
             return p[0] * m_4 * (v - erev);
         }
+        case HXO_SCA_LA: {
+            const double gca = p[4] * p[0] * s[0] * s[0] * s[1];
+            return (1e-4) * gca * (v - erev);
+        }
+        case HXO_CA: {
+            const double gCa = p[0] * s[0] * s[0] * s[1];
+            return gCa * (v - erev);
+        }
         default:
             return 0.0;
     }
@@ -279,6 +322,8 @@ static int chan_ion(int t) {
         case HXO_CA_HVA:
         case HXO_CA_LVAST:
         case HXO_IT2_LA:
+        case HXO_SCA_LA:
+        case HXO_CA:
             return 2;
         default:
             return 1;
@@ -370,6 +415,8 @@ void hxo_lib_init(const hxo_group* g, struct hxo_libstate* L, const double* v) {
                 case HXO_KCA_LA: kcala_rates(L->cai[L->ca_of[i]], p, g->dt, r); break;
                 case HXO_IT2_LA: it2la_trates(v[i] + p[1], p, g->dt, r); break;
                 case HXO_KDR_LA: kdrla_settables(v[i], r); r[0] = 0.0; break; /* m = minf; m = 0.0 */
+                case HXO_SCA_LA: scala_trates(v[i] + p[3], p, g->dt, r); break;
+                case HXO_CA: ca_rates(v[i], r); break;
             }
             s[0] = r[0];
             if (NST[t] == 2) s[1] = r[2];
@@ -466,6 +513,18 @@ void hxo_lib_state(const hxo_group* g, struct hxo_libstate* L, const double* v) 
                 it2la_trates(v[i] + p[1], p, dt, r);
                 s[0] = s[0] + r[1] * (r[0] - s[0]);
                 s[1] = s[1] + r[3] * (r[2] - s[1]);
+                continue;
+            }
+            if (t == HXO_SCA_LA) {
+                scala_trates(v[i] + p[3], p, dt, r);
+                s[0] = s[0] + r[1] * (r[0] - s[0]);
+                s[1] = s[1] + r[3] * (r[2] - s[1]);
+                continue;
+            }
+            if (t == HXO_CA) {
+                ca_rates(v[i], r);
+                s[0] = s[0] + (1.0 - exp(-dt / r[1])) * (r[0] - s[0]);
+                s[1] = s[1] + (1.0 - exp(-dt / r[3])) * (r[2] - s[1]);
                 continue;
             }
             if (t == HXO_KDR_LA) {
