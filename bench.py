@@ -25,10 +25,11 @@ The other configurations of the same metric (not the headline line):
   --config 5   302 cells coupled by 900 HalfGap pairs and 2000 graded
                synapses, 8000 steps (one step per launch);
   --config 6   library cells: --ncell random trees (default 1024, config-2
-               morphology) carrying the user-mech channel set with calcium
-               dynamics (NaTg, Nap_Et2, K_Pst, K_Tst, SKv3_1, SK_E2, Im,
-               Ca_HVA, Ca_LVAst, CaDynamics_E2, ions) and pas, 4000 steps,
-               gradients of every channel density and CaDynamics_E2 gamma.
+               morphology) carrying the user-mech channel set of a layer-5
+               pyramidal cell with calcium dynamics (NaTg, Nap_Et2, K_Pst,
+               K_Tst, SKv3_1, SK_E2, Im, Ca_HVA, Ca_LVAst, CaDynamics_E2,
+               ions) and pas, 4000 steps, gradients of every channel density
+               and CaDynamics_E2 gamma.
 """
 from __future__ import annotations
 
@@ -516,7 +517,7 @@ def build_workload(args, ws, rank):
                 "parallelism": "replicas only ({ws} GPU(s)): coupled every step"}
     if args.config == 6:
         seed0 = 51000 + 100000 * rank
-        g = synth.lib_tree_batch(args.ncell, seed0=seed0, nmin=200, nmax=1000)
+        g = synth.lib_tree_batch(args.ncell, seed0=seed0, nmin=200, nmax=1000, channels=synth.LIB_BBP_CHANNELS)
         keys = ("NaTg.gNaTgbar", "Nap_Et2.gNap_Et2bar", "K_Pst.gK_Pstbar", "K_Tst.gK_Tstbar", "SKv3_1.gSKv3_1bar",
                 "SK_E2.gSK_E2bar", "Im.gImbar", "Ca_HVA.gbar", "Ca_LVAst.gCa_LVAstbar", "CaDynamics_E2.gamma")
         return {"group": g, "teacher": synth.perturb_lib(g, 0.2, seed=seed0 + 7), "nstep": args.nstep, "keys": keys,

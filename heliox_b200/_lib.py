@@ -54,9 +54,15 @@ HX_P = {
     "kdr_la.gbar": 33,
     "sca_la.gbar": 34,
     "Ca.gCabar": 35,
+    "shl1_lr.w": 36,
+    "kvs1_lr.w": 37,
+    "irk_lr.w": 38,
+    "egl36_lr.w": 39,
+    "shk1_lr.w": 40,
+    "egl2_lr.w": 41,
 }
-HX_P_COUNT = 36
-HX_LIB_NTYPE = 20
+HX_P_COUNT = 42
+HX_LIB_NTYPE = 26
 
 
 class LibTable(C.Structure):

@@ -78,6 +78,12 @@ LIB_MECH_TABLE: List[Tuple[int, str, int, int, int, int, int, float]] = [
     (30, "kdr_la", 0, 0, 0, 8, 0, 0.0),
     (31, "sca_la", 0, 0, 0, 18, 0, 0.0),
     (32, "Ca", 0, 0, 0, 14, 0, 0.0),
+    (33, "shl1_lr", 0, 0, 0, 24, 0, 0.0),
+    (34, "kvs1_lr", 0, 0, 0, 20, 0, 0.0),
+    (35, "irk_lr", 0, 0, 0, 16, 0, 0.0),
+    (36, "egl36_lr", 0, 0, 0, 24, 0, 0.0),
+    (37, "shk1_lr", 0, 0, 0, 20, 0, 0.0),
+    (38, "egl2_lr", 0, 0, 0, 16, 0, 0.0),
 ]
 # data column of each library field (its var_in_coredata_idx); SK_E2.zTau is
 # the GLOBAL zTau_SK_E2 of globals.dat (SK_E2.cu:65-66)
@@ -90,6 +96,12 @@ LIB_COLUMNS = {
     "hd_la": {"ghdbar": 0, "vhalfl": 1, "tau": 2}, "km_la": {"gbar": 0}, "kca_la": {"gbar": 0},
     "it2_la": {"gcabar": 0}, "kdr_la": {"gbar": 0}, "sca_la": {"inactF": 0, "actF": 1, "gbar": 2},
     "Ca": {"gCabar": 0},
+    "shl1_lr": {"gbshl1": 0, "ek_tmp": 1, "w": 2, "dv": 3},
+    "kvs1_lr": {"gbkvs1": 0, "ek_tmp": 1, "w": 2, "dv": 3},
+    "irk_lr": {"gbirk": 0, "ek_tmp": 1, "w": 2, "dv": 3},
+    "egl36_lr": {"gbegl36": 0, "ek_tmp": 1, "w": 2, "dv": 3},
+    "shk1_lr": {"gbshk1": 0, "ek_tmp": 1, "w": 2, "dv": 3},
+    "egl2_lr": {"gbegl2": 0, "ek_tmp": 1, "w": 2, "dv": 3},
 }
 # GLOBALs the loader requires of a mechanism that the dynamics do not read
 # (km_la.cu:70-80: its table parameters), written with these values

@@ -650,6 +650,121 @@ struct CaPlain {
     }
 };
 
+// worm-lr channels (src/mech/worm-lr-mech/<name>.cu): current
+// w (gb gates (v - ek_tmp)) with the trainable weight w = p[0]; f = gb, ek_tmp,
+// dv, then the kinetics GLOBALs g[] in the mechanism's order; steady states
+// and time constants from setparames at v (the LRDS shadow gates of the
+// reference, advanced at v + dv, never reach v and are not carried).
+struct WormBase {
+    static constexpr int kP = 1, kIon = 3;
+    static constexpr bool kCai = false;
+    static constexpr int kErevFix = 1;
+};
+template <class T>
+__device__ __forceinline__ T sig_up(const T& v, double vh, double k) {  // 1 / (1 + exp(-(v - vh) / k))
+    return rcp(1.0 + exp(-(v - vh) * rcp(k)));
+}
+template <class T>
+__device__ __forceinline__ T sig_dn(const T& v, double vh, double k) {  // 1 / (1 + exp((v - vh) / k))
+    return rcp(1.0 + exp((v - vh) * rcp(k)));
+}
+template <class T>  // a / (exp(-(v - b)/c) + exp((v - d)/e)) + f
+__device__ __forceinline__ T bell(const T& v, double a, double b, double c, double d, double e, double f) {
+    return a * rcp(exp(-(v - b) * rcp(c)) + exp((v - d) * rcp(e))) + f;
+}
+struct Shl1Lr : WormBase {  // shl1_lr.cu
+    static constexpr int kS = 3;
+    template <class T>
+    __device__ static T cur(const T& v, const T* s, const T* p, const double* f, const T& e) {
+        return p[0] * (f[0] * s[0] * s[0] * s[0] * (0.7 * s[1] + 0.3 * s[2]) * (v - e));
+    }
+    template <class T>
+    __device__ static void gates(const T& v, const double* f, const T&, T* r) {
+        const double* g = f + 3;
+        const T hinf = sig_dn(v, g[2], g[3]);
+        r[0] = sig_up(v, g[0], g[1]);
+        r[1] = bell(v, g[4], g[5], g[6], g[7], g[8], g[9]) * 0.4;
+        r[2] = hinf;
+        r[3] = (g[10] * sig_dn(v, g[11], g[12]) + g[13]) * 0.08;
+        r[4] = hinf;
+        r[5] = (g[14] * sig_dn(v, g[15], g[16]) + g[17]) * 0.3;
+    }
+};
+struct Kvs1Lr : WormBase {  // kvs1_lr.cu
+    static constexpr int kS = 2;
+    template <class T>
+    __device__ static T cur(const T& v, const T* s, const T* p, const double* f, const T& e) {
+        return p[0] * (f[0] * s[0] * s[1] * (v - e));
+    }
+    template <class T>
+    __device__ static void gates(const T& v, const double* f, const T&, T* r) {
+        const double* g = f + 3;
+        r[0] = sig_up(v, g[0], g[1]);
+        r[1] = g[4] * sig_dn(v, g[5], g[6]) + g[7];
+        r[2] = sig_dn(v, g[2], g[3]);
+        r[3] = g[8] * sig_dn(v, g[9], g[10]) + g[11];
+    }
+};
+struct IrkLr : WormBase {  // irk_lr.cu
+    static constexpr int kS = 1;
+    template <class T>
+    __device__ static T cur(const T& v, const T* s, const T* p, const double* f, const T& e) {
+        return p[0] * (f[0] * s[0] * (v - e));
+    }
+    template <class T>
+    __device__ static void gates(const T& v, const double* f, const T&, T* r) {
+        const double* g = f + 3;
+        r[0] = sig_dn(v, g[0], g[1]);
+        r[1] = bell(v, g[2], g[3], g[4], g[5], g[6], g[7]);
+    }
+};
+struct Egl36Lr : WormBase {  // egl36_lr.cu: time constants atmf, atmm, atms
+    static constexpr int kS = 3;
+    template <class T>
+    __device__ static T cur(const T& v, const T* s, const T* p, const double* f, const T& e) {
+        return p[0] * (f[0] * (0.33 * s[0] + 0.36 * s[1] + 0.39 * s[2]) * (v - e));
+    }
+    template <class T>
+    __device__ static void gates(const T& v, const double* f, const T&, T* r) {
+        const double* g = f + 3;
+        const T inf = sig_up(v, g[0], g[1]);
+        r[0] = inf;
+        r[1] = T(g[4]);
+        r[2] = inf;
+        r[3] = T(g[3]);
+        r[4] = inf;
+        r[5] = T(g[2]);
+    }
+};
+struct Shk1Lr : WormBase {  // shk1_lr.cu
+    static constexpr int kS = 2;
+    template <class T>
+    __device__ static T cur(const T& v, const T* s, const T* p, const double* f, const T& e) {
+        return p[0] * (f[0] * s[0] * s[1] * (v - e));
+    }
+    template <class T>
+    __device__ static void gates(const T& v, const double* f, const T&, T* r) {
+        const double* g = f + 3;
+        r[0] = sig_up(v, g[0], g[1]);
+        r[1] = bell(v, g[4], g[5], g[6], g[7], g[8], g[9]);
+        r[2] = sig_dn(v, g[2], g[3]);
+        r[3] = T(g[10]);
+    }
+};
+struct Egl2Lr : WormBase {  // egl2_lr.cu
+    static constexpr int kS = 1;
+    template <class T>
+    __device__ static T cur(const T& v, const T* s, const T* p, const double* f, const T& e) {
+        return p[0] * (f[0] * s[0] * (v - e));
+    }
+    template <class T>
+    __device__ static void gates(const T& v, const double* f, const T&, T* r) {
+        const double* g = f + 3;
+        r[0] = sig_up(v, g[0], g[1]);
+        r[1] = g[2] * sig_dn(v, g[3], g[4]) + g[5];
+    }
+};
+
 // CaDynamics_E2.cu:101-137: cai' from cai and the step's calcium current.
 // The reference's steady term -(drive - (-minCai)/decay) / (-1/decay)
 // equals drive decay + minCai.
@@ -666,7 +781,7 @@ __device__ __forceinline__ T cadyn(const T& cai, const T& ica, const T& gamma, c
 // ------------------------------------------------------------ type table
 enum LibType : int {
     kNaIon = 0, kKIon, kCaIon, kCaDyn, kCaHVA, kCaLVAst, kIm, kKPst, kKTst, kNaTg, kNapEt2, kSKE2, kSKv31, kHdLa,
-    kKmLa, kKcaLa, kIt2La, kKdrLa, kScaLa, kCaPlain, kNType
+    kKmLa, kKcaLa, kIt2La, kKdrLa, kScaLa, kCaPlain, kShl1Lr, kKvs1Lr, kIrkLr, kEgl36Lr, kShk1Lr, kEgl2Lr, kNType
 };
 static_assert(kNType <= 32, "the per-node type mask (DevLib::mask) holds one bit per type");
 // first trainable kind of each type, relative to HX_P_CADYN_GAMMA (-1: none)
@@ -676,13 +791,17 @@ __host__ __device__ constexpr int kind0(int t) {
 // states per entry / fixed parameters per entry / trainable parameters per instance
 __host__ __device__ constexpr int nstate(int t) {
     return t == kCaIon ? 1
-           : (t == kIm || t == kSKE2 || t == kSKv31 || t == kHdLa || t == kKmLa || t == kKcaLa || t == kKdrLa) ? 1
+           : (t == kShl1Lr || t == kEgl36Lr) ? 3
+           : (t == kIm || t == kSKE2 || t == kSKv31 || t == kHdLa || t == kKmLa || t == kKcaLa || t == kKdrLa ||
+              t == kIrkLr || t == kEgl2Lr)
+               ? 1
            : t >= kCaHVA ? 2
                          : 0;
 }
 __host__ __device__ constexpr int nfix(int t) {
     return (t == kNaIon || t == kKIon) ? 1 : t == kCaIon ? 4 : t == kNaTg ? 4 : t == kSKE2 ? 1 : t == kHdLa ? 9
-           : t == kKmLa ? 5 : t == kKcaLa ? 4 : t == kIt2La ? 15 : t == kScaLa ? 4 : 0;
+           : t == kKmLa ? 5 : t == kKcaLa ? 4 : t == kIt2La ? 15 : t == kScaLa ? 4 : t == kShl1Lr ? 21
+           : t == kKvs1Lr ? 15 : t == kIrkLr ? 11 : t == kEgl36Lr ? 8 : t == kShk1Lr ? 14 : t == kEgl2Lr ? 9 : 0;
 }
 __host__ __device__ constexpr int ntrain(int t) { return t < kCaDyn ? 0 : t == kCaDyn ? 4 : 1; }
 
@@ -702,7 +821,13 @@ __host__ __device__ constexpr int ntrain(int t) { return t < kCaDyn ? 0 : t == k
     X(kIt2La, It2La)       \
     X(kKdrLa, KdrLa)       \
     X(kScaLa, ScaLa)       \
-    X(kCaPlain, CaPlain)
+    X(kCaPlain, CaPlain)   \
+    X(kShl1Lr, Shl1Lr)     \
+    X(kKvs1Lr, Kvs1Lr)     \
+    X(kIrkLr, IrkLr)       \
+    X(kEgl36Lr, Egl36Lr)   \
+    X(kShk1Lr, Shk1Lr)     \
+    X(kEgl2Lr, Egl2Lr)
 
 // ------------------------------------------------------------ drivers
 // one channel's forward contribution; returns I(v) (the ion current)

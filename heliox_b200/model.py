@@ -90,6 +90,14 @@ LIB_MECHS = (
     ("kdr_la", ("gbar",), 1),
     ("sca_la", ("gbar", "inactF", "actF", "vshift", "tadj"), 1),
     ("Ca", ("gCabar",), 1),
+    # worm-lr channels (src/mech/worm-lr-mech): current w * (gb * gates * (v - ek_tmp)); w is the weight the
+    # reference's LRDS learns, gb, ek_tmp, dv per instance, the kinetics GLOBALs
+    ("shl1_lr", ("w", "gbshl1", "ek_tmp", "dv", "vhm", "ka", "vhh", "ki", "atm", "btm", "ctm", "dtm", "etm", "ftm", "athf", "bthf", "cthf", "dthf", "aths", "bths", "cths", "dths"), 1),
+    ("kvs1_lr", ("w", "gbkvs1", "ek_tmp", "dv", "vhm", "ka", "vhh", "ki", "atm", "btm", "ctm", "dtm", "ath", "bth", "cth", "dth"), 1),
+    ("irk_lr", ("w", "gbirk", "ek_tmp", "dv", "vhm", "ka", "atm", "btm", "ctm", "dtm", "etm", "ftm"), 1),
+    ("egl36_lr", ("w", "gbegl36", "ek_tmp", "dv", "vhm", "ka", "atms", "atmm", "atmf"), 1),
+    ("shk1_lr", ("w", "gbshk1", "ek_tmp", "dv", "vhm", "ka", "vhh", "ki", "atm", "btm", "ctm", "dtm", "etm", "ftm", "ath"), 1),
+    ("egl2_lr", ("w", "gbegl2", "ek_tmp", "dv", "vhm", "ka", "atm", "btm", "ctm", "dtm"), 1),
 )
 # fields that are GLOBALs of their mechanism in the reference (one value per
 # group, written to globals.dat as <field>_<mechanism>)
@@ -101,6 +109,12 @@ LIB_GLOBALS = {
     "it2_la": ("vshift", "v12m", "vwm", "v12h", "vwh", "am", "ah", "vm1", "vm2", "vh1", "vh2", "wm1", "wm2", "wh1",
                "wh2"),
     "sca_la": ("vshift", "tadj"),
+    "shl1_lr": ("vhm", "ka", "vhh", "ki", "atm", "btm", "ctm", "dtm", "etm", "ftm", "athf", "bthf", "cthf", "dthf", "aths", "bths", "cths", "dths",),
+    "kvs1_lr": ("vhm", "ka", "vhh", "ki", "atm", "btm", "ctm", "dtm", "ath", "bth", "cth", "dth",),
+    "irk_lr": ("vhm", "ka", "atm", "btm", "ctm", "dtm", "etm", "ftm",),
+    "egl36_lr": ("vhm", "ka", "atms", "atmm", "atmf",),
+    "shk1_lr": ("vhm", "ka", "vhh", "ki", "atm", "btm", "ctm", "dtm", "etm", "ftm", "ath",),
+    "egl2_lr": ("vhm", "ka", "atm", "btm", "ctm", "dtm",),
 }
 LIB_NAMES = tuple(m[0] for m in LIB_MECHS)
 LIB_FIELDS = {m[0]: m[1] for m in LIB_MECHS}
@@ -111,6 +125,12 @@ LIB_IONS = {
     "K_Tst": ("k",), "NaTg": ("na",), "Nap_Et2": ("na",), "SK_E2": ("k", "ca"), "SKv3_1": ("k",),
     "hd_la": (), "km_la": ("k",), "kca_la": ("k", "ca"), "it2_la": ("ca",), "kdr_la": ("k",), "sca_la": ("ca",),
     "Ca": ("ca",),
+    "shl1_lr": ("k",),
+    "kvs1_lr": ("k",),
+    "irk_lr": ("k",),
+    "egl36_lr": ("k",),
+    "shk1_lr": ("k",),
+    "egl2_lr": ("k",),
 }
 
 
@@ -385,7 +405,14 @@ def lib_par_matrix(g: "CellGroup", name: str) -> np.ndarray:
 LIB_STATES = {"ca_ion": ("cai",), "Ca_HVA": ("m", "h"), "Ca_LVAst": ("m", "h"), "Im": ("m",), "K_Pst": ("m", "h"),
               "K_Tst": ("m", "h"), "NaTg": ("m", "h"), "Nap_Et2": ("m", "h"), "SK_E2": ("z",), "SKv3_1": ("m",),
               "hd_la": ("l",), "km_la": ("n",), "kca_la": ("n",), "it2_la": ("m", "h"), "kdr_la": ("m",),
-              "sca_la": ("m", "h"), "Ca": ("m", "h")}
+              "sca_la": ("m", "h"), "Ca": ("m", "h"),
+              "shl1_lr": ("m", "hf", "hs",),
+              "kvs1_lr": ("m", "h",),
+              "irk_lr": ("m",),
+              "egl36_lr": ("mf", "mm", "ms",),
+              "shk1_lr": ("m", "h",),
+              "egl2_lr": ("m",),
+}
 
 
 def empty_table(names, inames=()) -> MechTable:

@@ -248,6 +248,13 @@ LIB_DENSITY = {
     "kdr_la": (0.0, 0.01, 0.0),
     "sca_la": (0.0, 0.0, 0.5),  # pS/um^2
     "Ca": (2e-4, 0.0, 0.0),
+    # worm-lr channels: gb per region (w = 1 times the seeded lognormal factor)
+    "shl1_lr": (1e-3, 0.0, 0.0),
+    "kvs1_lr": (0.0, 0.0, 5e-5),
+    "irk_lr": (1e-4, 0.0, 1e-4),
+    "egl36_lr": (0.0, 0.0, 1e-4),
+    "shk1_lr": (5e-4, 5e-4, 0.0),
+    "egl2_lr": (0.0, 0.0, 5e-5),
 }
 # GLOBALs of hd_la / km_la (one value per group; their published defaults,
 # km_la's tadj = 2.3^((34 - 23) / 10)) and hd_la's per-instance vhalfl, tau
@@ -258,19 +265,35 @@ LIB_LA_GLOBALS = {
     "it2_la": dict(vshift=0.0, v12m=50.0, vwm=7.4, v12h=78.0, vwh=5.0, am=3.0, ah=85.0, vm1=25.0, vm2=100.0,
                    vh1=46.0, vh2=405.0, wm1=20.0, wm2=15.0, wh1=4.0, wh2=50.0),
     "sca_la": dict(vshift=0.0, tadj=2.3 ** 1.1),
+    # kinetics of the worm-lr channels (C. elegans K currents; voltages mV, times ms)
+    "shl1_lr": dict(vhm=-6.8, ka=14.1, vhh=-33.1, ki=8.3, atm=13.8, btm=-17.5, ctm=12.9, dtm=-3.7, etm=6.5, ftm=1.9,
+                    athf=539.0, bthf=-28.2, cthf=4.9, dthf=27.3, aths=8422.0, bths=-37.7, cths=6.4, dths=118.9),
+    "kvs1_lr": dict(vhm=57.1, ka=25.0, vhh=47.3, ki=11.1, atm=30.0, btm=18.1, ctm=20.0, dtm=1.0, ath=88.5, bth=50.0,
+                    cth=-15.0, dth=53.4),
+    "irk_lr": dict(vhm=-82.0, ka=13.0, atm=17.1, btm=-17.8, ctm=20.3, dtm=-43.4, etm=11.2, ftm=3.8),
+    "egl36_lr": dict(vhm=63.0, ka=28.5, atms=1000.0, atmm=100.0, atmf=13.0),
+    "shk1_lr": dict(vhm=20.4, ka=7.7, vhh=-7.0, ki=5.8, atm=26.6, btm=-33.7, ctm=15.8, dtm=-33.7, etm=15.4, ftm=2.0,
+                    ath=1400.0),
+    "egl2_lr": dict(vhm=-6.9, ka=14.9, atm=1845.8, btm=-122.6, ctm=13.8, dtm=1517.74),
 }
 LIB_CADYN = (dict(gamma=5e-4, decay=460.0), dict(gamma=5e-4, decay=100.0), dict(gamma=5e-4, decay=80.0))
 LIB_GBAR_FIELD = {nm: LIB_FIELDS[nm][0] for nm in LIB_DENSITY}
 
 
+# the user-mech set the library started from (a layer-5 pyramidal-cell
+# composition): bench config 6 uses it
+LIB_BBP_CHANNELS = ("NaTg", "Nap_Et2", "K_Pst", "K_Tst", "SKv3_1", "SK_E2", "Im", "Ca_HVA", "Ca_LVAst")
+
+
 def lib_tree_cell(seed: int, ncomp: int | None = None, nmin: int = 100, nmax: int = 400,
-                  amp: float | None = None) -> CellGroup:
+                  amp: float | None = None, channels=None) -> CellGroup:
     """One seeded random-tree cell carrying the user-mech channel set.
 
     The morphology is ``random_tree_cell``'s (soma, a 4-compartment axon
     initial segment, tapering dendrites).  Every compartment gets pas
     (g 3e-5, e -75); the channels of ``LIB_DENSITY`` (the user-mech set and
-    hd_la, km_la, kca_la, it2_la, kdr_la, sca_la, Ca, with the GLOBALs of
+    hd_la, km_la, kca_la, it2_la, kdr_la, sca_la, Ca and six worm-lr
+    channels, with the GLOBALs of
     ``LIB_LA_GLOBALS``) go where their region's density is nonzero, scaled
     by a seeded lognormal factor (sigma 0.1);
     CaDynamics_E2 sits with the Ca channels (depth 0.1 um, minCai 1e-4 mM);
@@ -278,6 +301,7 @@ def lib_tree_cell(seed: int, ncomp: int | None = None, nmin: int = 100, nmax: in
     them on (ca_ion: cai 5e-5, cao 2 mM, eca by the Nernst equation each
     step).  IClamp at the soma, del 5 ms, dur 50 ms, amplitude U[0.2, 1] nA.
     celsius 34 (the channels' temperature: their rate factors hard-code it).
+    ``channels``: the subset of ``LIB_DENSITY`` to place (default: all).
     """
     rng = np.random.default_rng(seed + 7_000_000)
     base = random_tree_cell(seed, ncomp=ncomp, nmin=nmin, nmax=nmax, amp=amp)
@@ -288,10 +312,15 @@ def lib_tree_cell(seed: int, ncomp: int | None = None, nmin: int = 100, nmax: in
     lib = {}
     need = {"na": np.zeros(n, bool), "k": np.zeros(n, bool), "ca": np.zeros(n, bool)}
     for nm, dens in LIB_DENSITY.items():
+        if channels is not None and nm not in channels:
+            continue
         d = np.asarray(dens)[region]
         nodes = np.nonzero(d > 0)[0]
         gbar = d[nodes] * np.exp(0.1 * rng.standard_normal(nodes.size))
         f = {LIB_GBAR_FIELD[nm]: _f64(gbar)}
+        if nm.endswith("_lr"):  # w (learned) carries the seeded factor, gb the region's density
+            f = {"w": _f64(gbar / d[nodes]), LIB_FIELDS[nm][1]: _f64(d[nodes]),
+                 "ek_tmp": _f64(np.full(nodes.size, -80.0)), "dv": _f64(np.full(nodes.size, 1e-3))}
         if nm == "NaTg":
             f.update(vshifth=_f64(np.zeros(nodes.size)), vshiftm=_f64(np.zeros(nodes.size)),
                      slopeh=_f64(np.full(nodes.size, 6.0)), slopem=_f64(np.full(nodes.size, 6.0)))

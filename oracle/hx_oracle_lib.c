@@ -21,6 +21,10 @@
  *   kdr_la                               src/mech/user-mech/kdr_la.cu:67-118
  *   sca_la (GLOBALs vshift, tadj)        src/mech/user-mech/sca_la.cu:95-160
  *   Ca                                   src/mech/user-mech/Ca.cu
+ *   shl1_lr, kvs1_lr, irk_lr, egl36_lr,  src/mech/worm-lr-mech/<name>.cu (setparames,
+ *   shk1_lr, egl2_lr                     current, state): i = w ik_tmp; the LRDS
+ *                                        shadow gates (m_dm, ...) never reach v and
+ *                                        are not carried
  * through MechTemp's finite-difference current (mech_template.cuh:589-648)
  * and the state phase order of nonvint_cpu (simulate.cpp:784-852: mechanisms
  * that write an ion in their state update first, then the others in type
@@ -36,8 +40,9 @@
 
 #define FD_EPS 0.001
 
-static const int NPAR[HXO_LIB_NTYPE] = {1, 1, 4, 4, 1, 1, 1, 1, 1, 5, 1, 2, 1, 11, 6, 5, 16, 1, 5, 1};
-static const int NST[HXO_LIB_NTYPE] = {0, 0, 0, 0, 2, 2, 1, 2, 2, 2, 2, 1, 1, 1, 1, 1, 2, 1, 2, 2};
+static const int NPAR[HXO_LIB_NTYPE] = {1, 1, 4, 4, 1, 1, 1, 1, 1, 5, 1, 2, 1, 11, 6, 5, 16, 1, 5, 1,
+                                        22, 16, 12, 9, 15, 10};
+static const int NST[HXO_LIB_NTYPE] = {0, 0, 0, 0, 2, 2, 1, 2, 2, 2, 2, 1, 1, 1, 1, 1, 2, 1, 2, 2, 3, 2, 1, 3, 2, 1};
 
 struct hxo_libstate {
     double* st[HXO_LIB_NTYPE]; /* n x NST per table */
@@ -251,6 +256,60 @@ static void ca_rates(double volt, double r[4]) {
     r[3] = 1.0 / (hA + hB);
 }
 
+/* worm-lr setparames at v: r = inf0, tau0, inf1, tau1, inf2, tau2 (the
+ * time constants the cnexp update uses).  g = the GLOBALs (p + 4). */
+static void worm_gates(int t, double v, const double* g, double r[6]) {
+    switch (t) {
+        case HXO_SHL1_LR: { /* vhm ka vhh ki atm btm ctm dtm etm ftm athf bthf cthf dthf aths bths cths dths */
+            const double minf = 1.0 / (1.0 + exp(-(v - g[0]) / g[1]));
+            const double hfinf = 1.0 / (1.0 + exp((v - g[2]) / g[3]));
+            const double hsinf = 1.0 / (1.0 + exp((v - g[2]) / g[3]));
+            const double tm = g[4] / (exp(-(v - g[5]) / g[6]) + exp((v - g[7]) / g[8])) + g[9];
+            const double thf = g[10] / (1.0 + exp((v - g[11]) / g[12])) + g[13];
+            const double ths = g[14] / (1.0 + exp((v - g[15]) / g[16])) + g[17];
+            r[0] = minf; r[1] = tm * 0.4;
+            r[2] = hfinf; r[3] = thf * 0.08;
+            r[4] = hsinf; r[5] = ths * 0.3;
+            break;
+        }
+        case HXO_KVS1_LR: { /* vhm ka vhh ki atm btm ctm dtm ath bth cth dth */
+            r[0] = 1.0 / (1.0 + exp(-(v - g[0]) / g[1]));
+            r[2] = 1.0 / (1.0 + exp((v - g[2]) / g[3]));
+            r[1] = g[4] / (1.0 + exp((v - g[5]) / g[6])) + g[7];
+            r[3] = g[8] / (1.0 + exp((v - g[9]) / g[10])) + g[11];
+            break;
+        }
+        case HXO_IRK_LR: { /* vhm ka atm btm ctm dtm etm ftm */
+            r[0] = 1.0 / (1.0 + exp((v - g[0]) / g[1]));
+            r[1] = g[2] / (exp(-(v - g[3]) / g[4]) + exp((v - g[5]) / g[6])) + g[7];
+            break;
+        }
+        case HXO_EGL36_LR: { /* vhm ka atms atmm atmf */
+            r[0] = 1.0 / (1.0 + exp(-(v - g[0]) / g[1]));
+            r[2] = 1.0 / (1.0 + exp(-(v - g[0]) / g[1]));
+            r[4] = 1.0 / (1.0 + exp(-(v - g[0]) / g[1]));
+            r[1] = g[4]; /* tmf = atmf */
+            r[3] = g[3]; /* tmm = atmm */
+            r[5] = g[2]; /* tms = atms */
+            break;
+        }
+        case HXO_SHK1_LR: { /* vhm ka vhh ki atm btm ctm dtm etm ftm ath */
+            r[0] = 1.0 / (1.0 + exp(-(v - g[0]) / g[1]));
+            r[2] = 1.0 / (1.0 + exp((v - g[2]) / g[3]));
+            r[1] = g[4] / (exp(-(v - g[5]) / g[6]) + exp((v - g[7]) / g[8])) + g[9];
+            r[3] = g[10];
+            break;
+        }
+        case HXO_EGL2_LR: { /* vhm ka atm btm ctm dtm */
+            r[0] = 1.0 / (1.0 + exp(-(v - g[0]) / g[1]));
+            r[1] = g[2] / (1.0 + exp((v - g[3]) / g[4])) + g[5];
+            break;
+        }
+    }
+}
+
+static int is_worm(int t) { return t >= HXO_SHL1_LR && t <= HXO_EGL2_LR; }
+
 static double sk_zinf(double ca) {
     double ca_safe = ca;
     if (ca_safe < 1e-7) ca_safe = ca_safe + 1e-07;
@@ -305,14 +364,35 @@ static double chan_current(int t, double v, const double* p, const double* s, do
             const double gCa = p[0] * s[0] * s[0] * s[1];
             return gCa * (v - erev);
         }
+        /* worm-lr: p = w, gb, ek_tmp, ...; ik_tmp = gb ... (v - ek_tmp), i = w ik_tmp */
+        case HXO_SHL1_LR: {
+            const double ik_tmp = p[1] * s[0] * s[0] * s[0] * (0.7 * s[1] + 0.3 * s[2]) * (v - erev);
+            return p[0] * ik_tmp;
+        }
+        case HXO_KVS1_LR:
+        case HXO_SHK1_LR: {
+            const double ik_tmp = p[1] * s[0] * s[1] * (v - erev);
+            return p[0] * ik_tmp;
+        }
+        case HXO_IRK_LR:
+        case HXO_EGL2_LR: {
+            const double ik_tmp = p[1] * s[0] * (v - erev);
+            return p[0] * ik_tmp;
+        }
+        case HXO_EGL36_LR: {
+            const double ik_tmp = p[1] * (0.33 * s[0] + 0.36 * s[1] + 0.39 * s[2]) * (v - erev);
+            return p[0] * ik_tmp;
+        }
         default:
             return 0.0;
     }
 }
 
 /* 0: na, 1: k, 2: ca (the ion whose erev a channel reads and current it writes),
- * 3: none (hd_la: its own reversal potential ehd, no ion current) */
+ * 3: none (hd_la: its own reversal potential ehd, no ion current), 4: its own
+ * reversal potential ek_tmp (the worm-lr channels; their k current is not read) */
 static int chan_ion(int t) {
+    if (is_worm(t)) return 4;
     switch (t) {
         case HXO_HD_LA:
             return 3;
@@ -418,6 +498,12 @@ void hxo_lib_init(const hxo_group* g, struct hxo_libstate* L, const double* v) {
                 case HXO_SCA_LA: scala_trates(v[i] + p[3], p, g->dt, r); break;
                 case HXO_CA: ca_rates(v[i], r); break;
             }
+            if (is_worm(t)) { /* every gate at its steady state */
+                double wr[6] = {0, 0, 0, 0, 0, 0};
+                worm_gates(t, v[i], p + 4, wr);
+                for (int q = 0; q < NST[t]; q++) s[q] = wr[2 * q];
+                continue;
+            }
             s[0] = r[0];
             if (NST[t] == 2) s[1] = r[2];
         }
@@ -441,7 +527,7 @@ void hxo_lib_current(const hxo_group* g, struct hxo_libstate* L, const double* v
             const int i = T->node[j];
             const double* p = T->par + NPAR[t] * j;
             const double* s = L->st[t] + NST[t] * j;
-            const double e = ion == 3 ? p[3] : ion_erev(L, ion, i);
+            const double e = ion == 3 ? p[3] : ion == 4 ? p[2] : ion_erev(L, ion, i);
             double gg = chan_current(t, v[i] + 0.001, p, s, e);
             const double r = chan_current(t, v[i], p, s, e);
             if (ion == 2) L->ica[L->ca_of[i]] += r;
@@ -513,6 +599,15 @@ void hxo_lib_state(const hxo_group* g, struct hxo_libstate* L, const double* v) 
                 it2la_trates(v[i] + p[1], p, dt, r);
                 s[0] = s[0] + r[1] * (r[0] - s[0]);
                 s[1] = s[1] + r[3] * (r[2] - s[1]);
+                continue;
+            }
+            if (is_worm(t)) { /* x + (1 - exp(dt ((-1) / tau))) (-(inf / tau) / ((-1) / tau) - x) */
+                double wr[6] = {0, 0, 0, 0, 0, 0};
+                worm_gates(t, v[i], p + 4, wr);
+                for (int q = 0; q < NST[t]; q++) {
+                    const double inf = wr[2 * q], tau = wr[2 * q + 1];
+                    s[q] = s[q] + (1.0 - exp(dt * ((-1.0) / tau))) * (-(inf / tau) / ((-1.0) / tau) - s[q]);
+                }
                 continue;
             }
             if (t == HXO_SCA_LA) {

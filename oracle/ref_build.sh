@@ -32,7 +32,8 @@ SRCS=$(cd "$REF" && ls \
   mech/user-mech/K_Pst.cu mech/user-mech/K_Tst.cu mech/user-mech/NaTg.cu mech/user-mech/Nap_Et2.cu \
   mech/user-mech/SK_E2.cu mech/user-mech/SKv3_1.cu mech/user-mech/hd_la.cu mech/user-mech/km_la.cu \
   mech/user-mech/kca_la.cu mech/user-mech/it2_la.cu mech/user-mech/kdr_la.cu mech/user-mech/sca_la.cu \
-  mech/user-mech/Ca.cu \
+  mech/user-mech/Ca.cu mech/worm-lr-mech/shl1_lr.cu mech/worm-lr-mech/kvs1_lr.cu mech/worm-lr-mech/irk_lr.cu \
+  mech/worm-lr-mech/egl36_lr.cu mech/worm-lr-mech/shk1_lr.cu mech/worm-lr-mech/egl2_lr.cu \
   2>/dev/null)
 
 compile() {
