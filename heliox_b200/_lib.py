@@ -60,9 +60,12 @@ HX_P = {
     "egl36_lr.w": 39,
     "shk1_lr.w": 40,
     "egl2_lr.w": 41,
+    "cca1_lr.w": 42,
+    "egl19_lr.w": 43,
+    "unc2_lr.w": 44,
 }
-HX_P_COUNT = 42
-HX_LIB_NTYPE = 26
+HX_P_COUNT = 45
+HX_LIB_NTYPE = 29
 
 
 class LibTable(C.Structure):

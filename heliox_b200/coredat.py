@@ -84,6 +84,9 @@ LIB_MECH_TABLE: List[Tuple[int, str, int, int, int, int, int, float]] = [
     (36, "egl36_lr", 0, 0, 0, 24, 0, 0.0),
     (37, "shk1_lr", 0, 0, 0, 20, 0, 0.0),
     (38, "egl2_lr", 0, 0, 0, 16, 0, 0.0),
+    (39, "cca1_lr", 0, 0, 0, 20, 0, 0.0),
+    (40, "egl19_lr", 0, 0, 0, 20, 0, 0.0),
+    (41, "unc2_lr", 0, 0, 0, 20, 0, 0.0),
 ]
 # data column of each library field (its var_in_coredata_idx); SK_E2.zTau is
 # the GLOBAL zTau_SK_E2 of globals.dat (SK_E2.cu:65-66)
@@ -102,6 +105,9 @@ LIB_COLUMNS = {
     "egl36_lr": {"gbegl36": 0, "ek_tmp": 1, "w": 2, "dv": 3},
     "shk1_lr": {"gbshk1": 0, "ek_tmp": 1, "w": 2, "dv": 3},
     "egl2_lr": {"gbegl2": 0, "ek_tmp": 1, "w": 2, "dv": 3},
+    "cca1_lr": {"gbcca1": 0, "eca_tmp": 1, "w": 2, "dv": 3},
+    "egl19_lr": {"gbegl19": 0, "eca_tmp": 1, "w": 2, "dv": 3},
+    "unc2_lr": {"gbunc2": 0, "eca_tmp": 1, "w": 2, "dv": 3},
 }
 # GLOBALs the loader requires of a mechanism that the dynamics do not read
 # (km_la.cu:70-80: its table parameters), written with these values

@@ -765,6 +765,69 @@ struct Egl2Lr : WormBase {  // egl2_lr.cu
     }
 };
 
+// worm-lr calcium channels: their own eca_tmp, the current w i_tmp goes into
+// the node's calcium current (ica)
+struct WormCaBase : WormBase {
+    static constexpr int kIonCur = 2;
+};
+struct Cca1Lr : WormCaBase {  // cca1_lr.cu (nrn_current_like, setparames)
+    static constexpr int kS = 2;
+    template <class T>
+    __device__ static T cur(const T& v, const T* s, const T* p, const double* f, const T& e) {
+        return p[0] * (f[0] * s[0] * s[0] * s[1] * (v - e));
+    }
+    template <class T>
+    __device__ static void gates(const T& v, const double* f, const T&, T* r) {
+        const double* g = f + 3;
+        r[0] = sig_up(v, g[0], g[1]);
+        r[1] = g[4] * sig_up(v, g[5], g[6]) + g[7];
+        r[2] = sig_dn(v, g[2], g[3]);
+        r[3] = g[8] * sig_dn(v, g[9], g[10]) + g[11];
+    }
+};
+struct Egl19Lr : WormCaBase {  // egl19_lr.cu
+    static constexpr int kS = 2;
+    template <class T>
+    __device__ static T cur(const T& v, const T* s, const T* p, const double* f, const T& e) {
+        return p[0] * (f[0] * s[0] * s[1] * (v - e));
+    }
+    template <class T>
+    __device__ static void gates(const T& v, const double* f, const T&, T* r) {
+        const double* g = f + 3;
+        r[0] = sig_up(v, g[0], g[1]);
+        r[2] = (g[6] * sig_up(v, g[2], g[3]) + g[7]) * (g[8] * sig_dn(v, g[4], g[5]) + g[9]);
+        const T y1 = (v - g[11]) * rcp(g[12]), y2 = (v - g[14]) * rcp(g[15]);
+        r[1] = g[10] * exp(-(y1 * y1)) + g[13] * exp(-(y2 * y2)) + g[16];
+        r[3] = g[17] * (g[18] * sig_dn(v, g[19], g[20]) + g[21] * sig_dn(v, g[22], g[23]) + g[24]);
+    }
+};
+struct Unc2Lr : WormCaBase {  // unc2_lr.cu
+    static constexpr int kS = 2;
+    template <class T>
+    __device__ static T cur(const T& v, const T* s, const T* p, const double* f, const T& e) {
+        return p[0] * (f[0] * s[0] * s[1] * (v - e));
+    }
+    template <class T>
+    __device__ static void gates(const T& v, const double* f, const T&, T* r) {
+        const double* g = f + 3;
+        r[0] = sig_up(v, g[0], g[1]);
+        r[2] = sig_dn(v, g[2], g[3]);
+        r[1] = bell(v, g[4], g[5], g[6], g[5], g[7], g[8]);
+        r[3] = g[9] * sig_up(v, g[10], g[11]) + g[12] * sig_dn(v, g[13], g[14]);
+    }
+};
+
+// the ion whose current a channel writes: kIonCur when it names one, else its
+// erev ion (0 Na, 1 K, 2 Ca; none for own-erev channels)
+template <class M, class = void>
+struct IonCur {
+    static constexpr int value = M::kIon <= 2 ? M::kIon : -1;
+};
+template <class M>
+struct IonCur<M, decltype((void)M::kIonCur)> {
+    static constexpr int value = M::kIonCur;
+};
+
 // CaDynamics_E2.cu:101-137: cai' from cai and the step's calcium current.
 // The reference's steady term -(drive - (-minCai)/decay) / (-1/decay)
 // equals drive decay + minCai.
@@ -781,7 +844,8 @@ __device__ __forceinline__ T cadyn(const T& cai, const T& ica, const T& gamma, c
 // ------------------------------------------------------------ type table
 enum LibType : int {
     kNaIon = 0, kKIon, kCaIon, kCaDyn, kCaHVA, kCaLVAst, kIm, kKPst, kKTst, kNaTg, kNapEt2, kSKE2, kSKv31, kHdLa,
-    kKmLa, kKcaLa, kIt2La, kKdrLa, kScaLa, kCaPlain, kShl1Lr, kKvs1Lr, kIrkLr, kEgl36Lr, kShk1Lr, kEgl2Lr, kNType
+    kKmLa, kKcaLa, kIt2La, kKdrLa, kScaLa, kCaPlain, kShl1Lr, kKvs1Lr, kIrkLr, kEgl36Lr, kShk1Lr, kEgl2Lr, kCca1Lr,
+    kEgl19Lr, kUnc2Lr, kNType
 };
 static_assert(kNType <= 32, "the per-node type mask (DevLib::mask) holds one bit per type");
 // first trainable kind of each type, relative to HX_P_CADYN_GAMMA (-1: none)
@@ -801,7 +865,8 @@ __host__ __device__ constexpr int nstate(int t) {
 __host__ __device__ constexpr int nfix(int t) {
     return (t == kNaIon || t == kKIon) ? 1 : t == kCaIon ? 4 : t == kNaTg ? 4 : t == kSKE2 ? 1 : t == kHdLa ? 9
            : t == kKmLa ? 5 : t == kKcaLa ? 4 : t == kIt2La ? 15 : t == kScaLa ? 4 : t == kShl1Lr ? 21
-           : t == kKvs1Lr ? 15 : t == kIrkLr ? 11 : t == kEgl36Lr ? 8 : t == kShk1Lr ? 14 : t == kEgl2Lr ? 9 : 0;
+           : t == kKvs1Lr ? 15 : t == kIrkLr ? 11 : t == kEgl36Lr ? 8 : t == kShk1Lr ? 14 : t == kEgl2Lr ? 9
+           : t == kCca1Lr ? 15 : t == kEgl19Lr ? 28 : t == kUnc2Lr ? 18 : 0;
 }
 __host__ __device__ constexpr int ntrain(int t) { return t < kCaDyn ? 0 : t == kCaDyn ? 4 : 1; }
 
@@ -827,7 +892,10 @@ __host__ __device__ constexpr int ntrain(int t) { return t < kCaDyn ? 0 : t == k
     X(kIrkLr, IrkLr)       \
     X(kEgl36Lr, Egl36Lr)   \
     X(kShk1Lr, Shk1Lr)     \
-    X(kEgl2Lr, Egl2Lr)
+    X(kEgl2Lr, Egl2Lr)     \
+    X(kCca1Lr, Cca1Lr)     \
+    X(kEgl19Lr, Egl19Lr)   \
+    X(kUnc2Lr, Unc2Lr)
 
 // ------------------------------------------------------------ drivers
 // one channel's forward contribution; returns I(v) (the ion current)
@@ -957,7 +1025,7 @@ __device__ __forceinline__ double lib_current(const DevLib& L, int gi, double v,
         const double p[1] = {__ldg(L.prm[kind0(T_)] + inst)};                       \
         const double e_ = M_::kIon == 0 ? ena : M_::kIon == 1 ? ek : M_::kIon == 2 ? eca : __ldg(f + M_::kErevFix); \
         const double i0 = fwd_cur<M_>(v, s, p, f, e_, r, dd);                       \
-        if (M_::kIon == 2) ica += i0;                                               \
+        if (IonCur<M_>::value == 2) ica += i0;                                      \
     } break;
                 HX_LIB_CHANNELS(HX_LIB_FWD)
 #undef HX_LIB_FWD
@@ -1118,7 +1186,7 @@ __device__ __forceinline__ double lib_current_adj(const DevLib& L, int gi, doubl
         const double p[1] = {__ldg(L.prm[kind0(T_)] + inst)};                                  \
         const double e_ = M_::kIon == 0 ? ena : M_::kIon == 1 ? ek : M_::kIon == 2 ? eca : __ldg(f + M_::kErevFix); \
         double gp[1] = {0.0}, le = 0.0;                                                        \
-        lv += vjp_cur<M_>(v, Xk + so, p, f, e_, w, ld, M_::kIon == 2 ? lica : 0.0, lam + so,   \
+        lv += vjp_cur<M_>(v, Xk + so, p, f, e_, w, ld, IonCur<M_>::value == 2 ? lica : 0.0, lam + so, \
                           gp, le);                                                             \
         L.grad[kind0(T_)][inst] += gp[0];                                                      \
         if (M_::kIon == 2) leca += le;                                                         \

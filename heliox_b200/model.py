@@ -98,6 +98,9 @@ LIB_MECHS = (
     ("egl36_lr", ("w", "gbegl36", "ek_tmp", "dv", "vhm", "ka", "atms", "atmm", "atmf"), 1),
     ("shk1_lr", ("w", "gbshk1", "ek_tmp", "dv", "vhm", "ka", "vhh", "ki", "atm", "btm", "ctm", "dtm", "etm", "ftm", "ath"), 1),
     ("egl2_lr", ("w", "gbegl2", "ek_tmp", "dv", "vhm", "ka", "atm", "btm", "ctm", "dtm"), 1),
+    ("cca1_lr", ("w", "gbcca1", "eca_tmp", "dv", "vhm", "ka", "vhh", "ki", "atm", "btm", "ctm", "dtm", "ath", "bth", "cth", "dth"), 1),
+    ("egl19_lr", ("w", "gbegl19", "eca_tmp", "dv", "vhm", "ka", "vhh", "ki", "vhhb", "kib", "ahinf", "bhinf", "chinf", "dhinf", "atm", "btm", "ctm", "dtm", "etm", "ftm", "gtm", "ath", "bth", "cth", "dth", "eth", "fth", "gth", "hth"), 1),
+    ("unc2_lr", ("w", "gbunc2", "eca_tmp", "dv", "vhm", "ka", "vhh", "ki", "atm", "btm", "ctm", "dtm", "etm", "ath", "bth", "cth", "dth", "eth", "fth"), 1),
 )
 # fields that are GLOBALs of their mechanism in the reference (one value per
 # group, written to globals.dat as <field>_<mechanism>)
@@ -115,6 +118,9 @@ LIB_GLOBALS = {
     "egl36_lr": ("vhm", "ka", "atms", "atmm", "atmf",),
     "shk1_lr": ("vhm", "ka", "vhh", "ki", "atm", "btm", "ctm", "dtm", "etm", "ftm", "ath",),
     "egl2_lr": ("vhm", "ka", "atm", "btm", "ctm", "dtm",),
+    "cca1_lr": ("vhm", "ka", "vhh", "ki", "atm", "btm", "ctm", "dtm", "ath", "bth", "cth", "dth",),
+    "egl19_lr": ("vhm", "ka", "vhh", "ki", "vhhb", "kib", "ahinf", "bhinf", "chinf", "dhinf", "atm", "btm", "ctm", "dtm", "etm", "ftm", "gtm", "ath", "bth", "cth", "dth", "eth", "fth", "gth", "hth",),
+    "unc2_lr": ("vhm", "ka", "vhh", "ki", "atm", "btm", "ctm", "dtm", "etm", "ath", "bth", "cth", "dth", "eth", "fth",),
 }
 LIB_NAMES = tuple(m[0] for m in LIB_MECHS)
 LIB_FIELDS = {m[0]: m[1] for m in LIB_MECHS}
@@ -131,6 +137,9 @@ LIB_IONS = {
     "egl36_lr": ("k",),
     "shk1_lr": ("k",),
     "egl2_lr": ("k",),
+    "cca1_lr": ("ca",),
+    "egl19_lr": ("ca",),
+    "unc2_lr": ("ca",),
 }
 
 
@@ -412,6 +421,9 @@ LIB_STATES = {"ca_ion": ("cai",), "Ca_HVA": ("m", "h"), "Ca_LVAst": ("m", "h"), 
               "egl36_lr": ("mf", "mm", "ms",),
               "shk1_lr": ("m", "h",),
               "egl2_lr": ("m",),
+              "cca1_lr": ("m", "h"),
+              "egl19_lr": ("m", "h"),
+              "unc2_lr": ("m", "h"),
 }
 
 

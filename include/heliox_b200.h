@@ -54,20 +54,25 @@ typedef struct hx_ctx hx_ctx;
  *   HX_LIB_SCA_LA (sca_la.cu): gbar (pS/um2), inactF, actF, then its GLOBALs
  *                  vshift, tadj
  *   HX_LIB_CA (Ca.cu): gCabar
- *   HX_LIB_SHL1_LR .. HX_LIB_EGL2_LR (src/mech/worm-lr-mech/<name>.cu): w,
- *                  gb, ek_tmp, dv, then the kinetics GLOBALs in the
+ *   HX_LIB_SHL1_LR .. HX_LIB_UNC2_LR (src/mech/worm-lr-mech/<name>.cu): w,
+ *                  gb, ek_tmp (eca_tmp for cca1_lr, egl19_lr, unc2_lr, whose
+ *                  current enters ica), dv, then the kinetics GLOBALs in the
  *                  mechanism's order (shl1_lr: vhm ka vhh ki atm btm ctm dtm
  *                  etm ftm athf bthf cthf dthf aths bths cths dths; kvs1_lr:
  *                  vhm ka vhh ki atm btm ctm dtm ath bth cth dth; irk_lr: vhm
  *                  ka atm btm ctm dtm etm ftm; egl36_lr: vhm ka atms atmm atmf;
  *                  shk1_lr: vhm ka vhh ki atm btm ctm dtm etm ftm ath; egl2_lr:
- *                  vhm ka atm btm ctm dtm); current w (gb gates (v - ek_tmp)),
+ *                  vhm ka atm btm ctm dtm; cca1_lr: vhm ka vhh ki atm btm ctm
+ *                  dtm ath bth cth dth; egl19_lr: vhm ka vhh ki vhhb kib ahinf
+ *                  bhinf chinf dhinf atm btm ctm dtm etm ftm gtm ath bth cth dth
+ *                  eth fth gth hth; unc2_lr: vhm ka vhh ki atm btm ctm dtm etm
+ *                  ath bth cth dth eth fth); current w (gb gates (v - ek_tmp)),
  *                  w the trainable weight
  * A channel needs its ion on its node (Na: NaTg, Nap_Et2; K: Im, K_Pst,
  * K_Tst, SK_E2, SKv3_1, km_la, kca_la, kdr_la; Ca: CaDynamics_E2, Ca_HVA,
  * Ca_LVAst, it2_la, sca_la, Ca, SK_E2 and kca_la (cai)); the worm-lr
- * channels need k_ion on their node (the reference maps their k current) but
- * use their own ek_tmp; hd_la's current is nonspecific
+ * channels need k_ion (ca_ion for cca1_lr, egl19_lr, unc2_lr) on their node
+ * (the reference maps their ion current) but use their own ek_tmp / eca_tmp; hd_la's current is nonspecific
  * (its own ehd);
  * na_ion / k_ion on an hh node carry hh's ena / ek. */
 enum hx_lib_type {
@@ -97,7 +102,10 @@ enum hx_lib_type {
     HX_LIB_EGL36_LR = 23,
     HX_LIB_SHK1_LR = 24,
     HX_LIB_EGL2_LR = 25,
-    HX_LIB_NTYPE = 26
+    HX_LIB_CCA1_LR = 26,
+    HX_LIB_EGL19_LR = 27,
+    HX_LIB_UNC2_LR = 28,
+    HX_LIB_NTYPE = 29
 };
 typedef struct hx_lib_table {
     int n;
@@ -211,7 +219,10 @@ enum hx_param_kind {
     HX_P_EGL36_LR_W = 39,
     HX_P_SHK1_LR_W = 40,
     HX_P_EGL2_LR_W = 41,
-    HX_P_COUNT = 42
+    HX_P_CCA1_LR_W = 42,
+    HX_P_EGL19_LR_W = 43,
+    HX_P_UNC2_LR_W = 44,
+    HX_P_COUNT = 45
 };
 
 /* Statistics of the execution plan built at load time. */

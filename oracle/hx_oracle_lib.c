@@ -22,7 +22,8 @@
  *   sca_la (GLOBALs vshift, tadj)        src/mech/user-mech/sca_la.cu:95-160
  *   Ca                                   src/mech/user-mech/Ca.cu
  *   shl1_lr, kvs1_lr, irk_lr, egl36_lr,  src/mech/worm-lr-mech/<name>.cu (setparames,
- *   shk1_lr, egl2_lr                     current, state): i = w ik_tmp; the LRDS
+ *   shk1_lr, egl2_lr, cca1_lr, egl19_lr, current, state): i = w ik_tmp; the LRDS
+ *   unc2_lr (calcium: i into ica)
  *                                        shadow gates (m_dm, ...) never reach v and
  *                                        are not carried
  * through MechTemp's finite-difference current (mech_template.cuh:589-648)
@@ -41,8 +42,9 @@
 #define FD_EPS 0.001
 
 static const int NPAR[HXO_LIB_NTYPE] = {1, 1, 4, 4, 1, 1, 1, 1, 1, 5, 1, 2, 1, 11, 6, 5, 16, 1, 5, 1,
-                                        22, 16, 12, 9, 15, 10};
-static const int NST[HXO_LIB_NTYPE] = {0, 0, 0, 0, 2, 2, 1, 2, 2, 2, 2, 1, 1, 1, 1, 1, 2, 1, 2, 2, 3, 2, 1, 3, 2, 1};
+                                        22, 16, 12, 9, 15, 10, 16, 29, 19};
+static const int NST[HXO_LIB_NTYPE] = {0, 0, 0, 0, 2, 2, 1, 2, 2, 2, 2, 1, 1, 1, 1, 1, 2, 1, 2, 2,
+                                       3, 2, 1, 3, 2, 1, 2, 2, 2};
 
 struct hxo_libstate {
     double* st[HXO_LIB_NTYPE]; /* n x NST per table */
@@ -305,10 +307,33 @@ static void worm_gates(int t, double v, const double* g, double r[6]) {
             r[1] = g[2] / (1.0 + exp((v - g[3]) / g[4])) + g[5];
             break;
         }
+        case HXO_CCA1_LR: { /* vhm ka vhh ki atm btm ctm dtm ath bth cth dth */
+            r[0] = 1.0 / (1.0 + exp(-(v - g[0]) / g[1]));
+            r[2] = 1.0 / (1.0 + exp((v - g[2]) / g[3]));
+            r[1] = g[4] / (1.0 + exp(-(v - g[5]) / g[6])) + g[7];
+            r[3] = g[8] / (1.0 + exp((v - g[9]) / g[10])) + g[11];
+            break;
+        }
+        case HXO_EGL19_LR: { /* vhm ka vhh ki vhhb kib ahinf bhinf chinf dhinf atm btm ctm dtm etm ftm gtm
+                                ath bth cth dth eth fth gth hth */
+            r[0] = 1.0 / (1.0 + exp(-(v - g[0]) / g[1]));
+            r[2] = (g[6] / (1.0 + exp(-(v - g[2]) / g[3])) + g[7]) * (g[8] / (1.0 + exp((v - g[4]) / g[5])) + g[9]);
+            r[1] = g[10] * exp(-pow((v - g[11]) / g[12], 2.0)) + g[13] * exp(-pow((v - g[14]) / g[15], 2.0)) + g[16];
+            r[3] = g[17] * ((g[18] / (1.0 + exp((v - g[19]) / g[20]))) + (g[21] / (1.0 + exp((v - g[22]) / g[23]))) +
+                            g[24]);
+            break;
+        }
+        case HXO_UNC2_LR: { /* vhm ka vhh ki atm btm ctm dtm etm ath bth cth dth eth fth */
+            r[0] = 1.0 / (1.0 + exp(-(v - g[0]) / g[1]));
+            r[2] = 1.0 / (1.0 + exp((v - g[2]) / g[3]));
+            r[1] = g[4] / (exp(-(v - g[5]) / g[6]) + exp((v - g[5]) / g[7])) + g[8];
+            r[3] = g[9] / (1.0 + exp(-(v - g[10]) / g[11])) + g[12] / (1.0 + exp((v - g[13]) / g[14]));
+            break;
+        }
     }
 }
 
-static int is_worm(int t) { return t >= HXO_SHL1_LR && t <= HXO_EGL2_LR; }
+static int is_worm(int t) { return t >= HXO_SHL1_LR && t <= HXO_UNC2_LR; }
 
 static double sk_zinf(double ca) {
     double ca_safe = ca;
@@ -382,6 +407,15 @@ static double chan_current(int t, double v, const double* p, const double* s, do
         case HXO_EGL36_LR: {
             const double ik_tmp = p[1] * (0.33 * s[0] + 0.36 * s[1] + 0.39 * s[2]) * (v - erev);
             return p[0] * ik_tmp;
+        }
+        case HXO_CCA1_LR: {
+            const double ica_tmp = p[1] * s[0] * s[0] * s[1] * (v - erev);
+            return p[0] * ica_tmp;
+        }
+        case HXO_EGL19_LR:
+        case HXO_UNC2_LR: {
+            const double ica_tmp = p[1] * s[0] * s[1] * (v - erev);
+            return p[0] * ica_tmp;
         }
         default:
             return 0.0;
@@ -530,7 +564,7 @@ void hxo_lib_current(const hxo_group* g, struct hxo_libstate* L, const double* v
             const double e = ion == 3 ? p[3] : ion == 4 ? p[2] : ion_erev(L, ion, i);
             double gg = chan_current(t, v[i] + 0.001, p, s, e);
             const double r = chan_current(t, v[i], p, s, e);
-            if (ion == 2) L->ica[L->ca_of[i]] += r;
+            if (ion == 2 || t >= HXO_CCA1_LR) L->ica[L->ca_of[i]] += r; /* worm-lr calcium: i into ica */
             gg = (gg - r) / FD_EPS;
             rhs[i] -= r;
             d[i] += gg;

@@ -34,6 +34,7 @@ SRCS=$(cd "$REF" && ls \
   mech/user-mech/kca_la.cu mech/user-mech/it2_la.cu mech/user-mech/kdr_la.cu mech/user-mech/sca_la.cu \
   mech/user-mech/Ca.cu mech/worm-lr-mech/shl1_lr.cu mech/worm-lr-mech/kvs1_lr.cu mech/worm-lr-mech/irk_lr.cu \
   mech/worm-lr-mech/egl36_lr.cu mech/worm-lr-mech/shk1_lr.cu mech/worm-lr-mech/egl2_lr.cu \
+  mech/worm-lr-mech/cca1_lr.cu mech/worm-lr-mech/egl19_lr.cu mech/worm-lr-mech/unc2_lr.cu \
   2>/dev/null)
 
 compile() {
