@@ -63,9 +63,11 @@ HX_P = {
     "cca1_lr.w": 42,
     "egl19_lr.w": 43,
     "unc2_lr.w": 44,
+    "kcnl_lr.w": 45,
+    "nca_lr.w": 46,
 }
-HX_P_COUNT = 45
-HX_LIB_NTYPE = 29
+HX_P_COUNT = 47
+HX_LIB_NTYPE = 31
 
 
 class LibTable(C.Structure):

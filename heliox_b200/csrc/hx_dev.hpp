@@ -138,9 +138,9 @@ struct DevNet {
 // km_la: Ra, Rb, tha, qa, tadj; kca_la: Ra, Rb, caix, tadj; it2_la: vshift,
 // v12m, vwm, v12h, vwh, am, ah, vm1, vm2, vh1, vh2, wm1, wm2, wh1, wh2;
 // sca_la: inactF, actF, vshift, tadj; worm-lr: gb, ek_tmp, dv, kinetics).  Trainable
-// parameters (HX_P_CADYN_GAMMA .. HX_P_UNC2_LR_W) live per instance in
+// parameters (HX_P_CADYN_GAMMA .. HX_P_NCA_LR_W) live per instance in
 // prm[kind - HX_P_CADYN_GAMMA], their gradients in grad[...].
-constexpr int kLibKinds = 29;
+constexpr int kLibKinds = 31;
 struct DevLib {
     int nst;
     const int *node_off, *ent, *ent_st, *ent_fix;  // node_off: nnode + 1; ent_st: nent + 1

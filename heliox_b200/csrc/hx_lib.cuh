@@ -817,6 +817,30 @@ struct Unc2Lr : WormCaBase {  // unc2_lr.cu
     }
 };
 
+struct KcnlLr : WormBase {  // kcnl_lr.cu: f = gb, dv, kca, a, ek_tmp (GLOBALs kca, a, ek_tmp)
+    static constexpr int kS = 1;
+    static constexpr bool kCai = true;
+    static constexpr int kErevFix = 4;
+    template <class T>
+    __device__ static T cur(const T& v, const T* s, const T* p, const double* f, const T& e) {
+        return p[0] * (f[0] * s[0] * (v - e));
+    }
+    template <class T>
+    __device__ static void gates(const T&, const double* f, const T& cai, T* r) {
+        r[0] = cai * rcp(f[2] + cai);
+        r[1] = T(f[3]);
+    }
+};
+struct NcaLr : WormBase {  // nca_lr.cu: a weighted leak, f = gb, ena_tmp
+    static constexpr int kS = 0;
+    template <class T>
+    __device__ static T cur(const T& v, const T*, const T* p, const double* f, const T& e) {
+        return p[0] * (f[0] * (v - e));
+    }
+    template <class T>
+    __device__ static void gates(const T&, const double*, const T&, T*) {}
+};
+
 // the ion whose current a channel writes: kIonCur when it names one, else its
 // erev ion (0 Na, 1 K, 2 Ca; none for own-erev channels)
 template <class M, class = void>
@@ -845,7 +869,7 @@ __device__ __forceinline__ T cadyn(const T& cai, const T& ica, const T& gamma, c
 enum LibType : int {
     kNaIon = 0, kKIon, kCaIon, kCaDyn, kCaHVA, kCaLVAst, kIm, kKPst, kKTst, kNaTg, kNapEt2, kSKE2, kSKv31, kHdLa,
     kKmLa, kKcaLa, kIt2La, kKdrLa, kScaLa, kCaPlain, kShl1Lr, kKvs1Lr, kIrkLr, kEgl36Lr, kShk1Lr, kEgl2Lr, kCca1Lr,
-    kEgl19Lr, kUnc2Lr, kNType
+    kEgl19Lr, kUnc2Lr, kKcnlLr, kNcaLr, kNType
 };
 static_assert(kNType <= 32, "the per-node type mask (DevLib::mask) holds one bit per type");
 // first trainable kind of each type, relative to HX_P_CADYN_GAMMA (-1: none)
@@ -855,9 +879,10 @@ __host__ __device__ constexpr int kind0(int t) {
 // states per entry / fixed parameters per entry / trainable parameters per instance
 __host__ __device__ constexpr int nstate(int t) {
     return t == kCaIon ? 1
+           : t == kNcaLr ? 0
            : (t == kShl1Lr || t == kEgl36Lr) ? 3
            : (t == kIm || t == kSKE2 || t == kSKv31 || t == kHdLa || t == kKmLa || t == kKcaLa || t == kKdrLa ||
-              t == kIrkLr || t == kEgl2Lr)
+              t == kIrkLr || t == kEgl2Lr || t == kKcnlLr)
                ? 1
            : t >= kCaHVA ? 2
                          : 0;
@@ -866,7 +891,7 @@ __host__ __device__ constexpr int nfix(int t) {
     return (t == kNaIon || t == kKIon) ? 1 : t == kCaIon ? 4 : t == kNaTg ? 4 : t == kSKE2 ? 1 : t == kHdLa ? 9
            : t == kKmLa ? 5 : t == kKcaLa ? 4 : t == kIt2La ? 15 : t == kScaLa ? 4 : t == kShl1Lr ? 21
            : t == kKvs1Lr ? 15 : t == kIrkLr ? 11 : t == kEgl36Lr ? 8 : t == kShk1Lr ? 14 : t == kEgl2Lr ? 9
-           : t == kCca1Lr ? 15 : t == kEgl19Lr ? 28 : t == kUnc2Lr ? 18 : 0;
+           : t == kCca1Lr ? 15 : t == kEgl19Lr ? 28 : t == kUnc2Lr ? 18 : t == kKcnlLr ? 5 : t == kNcaLr ? 2 : 0;
 }
 __host__ __device__ constexpr int ntrain(int t) { return t < kCaDyn ? 0 : t == kCaDyn ? 4 : 1; }
 
@@ -895,7 +920,9 @@ __host__ __device__ constexpr int ntrain(int t) { return t < kCaDyn ? 0 : t == k
     X(kEgl2Lr, Egl2Lr)     \
     X(kCca1Lr, Cca1Lr)     \
     X(kEgl19Lr, Egl19Lr)   \
-    X(kUnc2Lr, Unc2Lr)
+    X(kUnc2Lr, Unc2Lr)     \
+    X(kKcnlLr, KcnlLr)     \
+    X(kNcaLr, NcaLr)
 
 // ------------------------------------------------------------ drivers
 // one channel's forward contribution; returns I(v) (the ion current)
@@ -918,7 +945,7 @@ __device__ __forceinline__ double vjp_cur(double v, const double* s, const doubl
                                           double w, double ld, double li, double* ls, double* gp, double& le) {
     constexpr int N = 2 + M::kS + M::kP;
     using D = Dual<N>;
-    D ds[M::kS], dp[M::kP];
+    D ds[M::kS + 1], dp[M::kP];
 #pragma unroll
     for (int i = 0; i < M::kS; ++i) ds[i] = D::var(s[i], 1 + i);
 #pragma unroll
@@ -940,7 +967,7 @@ __device__ __forceinline__ double vjp_cur(double v, const double* s, const doubl
 // A channel's state phase: each gate x' = x + (1 - exp(-dt/tau)) (inf - x)
 template <class M>
 __device__ __forceinline__ void chan_state(double v, double dt, double* s, const double* f, double cai) {
-    double r[2 * M::kS];
+    double r[2 * M::kS + 1];
     M::template gates<double>(v, f, cai, r);
 #pragma unroll
     for (int j = 0; j < M::kS; ++j) s[j] = cnexp(s[j], r[2 * j], r[2 * j + 1], dt);
@@ -957,7 +984,7 @@ struct InitZero<M, decltype((void)M::kInitZero)> {
 };
 template <class M>
 __device__ __forceinline__ void chan_init(double v, double* s, const double* f, double cai) {
-    double r[2 * M::kS];
+    double r[2 * M::kS + 1];
     M::template gates<double>(v, f, cai, r);
 #pragma unroll
     for (int j = 0; j < M::kS; ++j) s[j] = InitZero<M>::value ? 0.0 : r[2 * j];
@@ -975,7 +1002,7 @@ __device__ __forceinline__ double vjp_state(double v1, double dt, const double* 
     using D = Dual<N>;
     const D dv = D::var(v1, 0);
     const D dc = M::kCai ? D::var(cai, N - 1) : D(cai);
-    D r[2 * M::kS];
+    D r[2 * M::kS + 1];
     M::template gates<D>(dv, f, dc, r);
     double mu = 0.0;
 #pragma unroll

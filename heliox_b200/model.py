@@ -101,6 +101,8 @@ LIB_MECHS = (
     ("cca1_lr", ("w", "gbcca1", "eca_tmp", "dv", "vhm", "ka", "vhh", "ki", "atm", "btm", "ctm", "dtm", "ath", "bth", "cth", "dth"), 1),
     ("egl19_lr", ("w", "gbegl19", "eca_tmp", "dv", "vhm", "ka", "vhh", "ki", "vhhb", "kib", "ahinf", "bhinf", "chinf", "dhinf", "atm", "btm", "ctm", "dtm", "etm", "ftm", "gtm", "ath", "bth", "cth", "dth", "eth", "fth", "gth", "hth"), 1),
     ("unc2_lr", ("w", "gbunc2", "eca_tmp", "dv", "vhm", "ka", "vhh", "ki", "atm", "btm", "ctm", "dtm", "etm", "ath", "bth", "cth", "dth", "eth", "fth"), 1),
+    ("kcnl_lr", ("w", "gbkcnl", "dv", "kca", "a", "ek_tmp"), 1),
+    ("nca_lr", ("w", "gbnca", "ena_tmp"), 1),
 )
 # fields that are GLOBALs of their mechanism in the reference (one value per
 # group, written to globals.dat as <field>_<mechanism>)
@@ -121,6 +123,7 @@ LIB_GLOBALS = {
     "cca1_lr": ("vhm", "ka", "vhh", "ki", "atm", "btm", "ctm", "dtm", "ath", "bth", "cth", "dth",),
     "egl19_lr": ("vhm", "ka", "vhh", "ki", "vhhb", "kib", "ahinf", "bhinf", "chinf", "dhinf", "atm", "btm", "ctm", "dtm", "etm", "ftm", "gtm", "ath", "bth", "cth", "dth", "eth", "fth", "gth", "hth",),
     "unc2_lr": ("vhm", "ka", "vhh", "ki", "atm", "btm", "ctm", "dtm", "etm", "ath", "bth", "cth", "dth", "eth", "fth",),
+    "kcnl_lr": ("kca", "a", "ek_tmp"),
 }
 LIB_NAMES = tuple(m[0] for m in LIB_MECHS)
 LIB_FIELDS = {m[0]: m[1] for m in LIB_MECHS}
@@ -140,6 +143,8 @@ LIB_IONS = {
     "cca1_lr": ("ca",),
     "egl19_lr": ("ca",),
     "unc2_lr": ("ca",),
+    "kcnl_lr": ("k", "ca"),
+    "nca_lr": ("na",),
 }
 
 
@@ -424,6 +429,7 @@ LIB_STATES = {"ca_ion": ("cai",), "Ca_HVA": ("m", "h"), "Ca_LVAst": ("m", "h"), 
               "cca1_lr": ("m", "h"),
               "egl19_lr": ("m", "h"),
               "unc2_lr": ("m", "h"),
+              "kcnl_lr": ("m",),
 }
 
 

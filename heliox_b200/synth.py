@@ -258,6 +258,8 @@ LIB_DENSITY = {
     "cca1_lr": (0.0, 0.0, 1e-5),
     "egl19_lr": (0.0, 0.0, 1e-5),
     "unc2_lr": (0.0, 0.0, 1e-5),
+    "kcnl_lr": (1e-4, 0.0, 1e-5),
+    "nca_lr": (0.0, 0.0, 2e-6),
 }
 # GLOBALs of hd_la / km_la (one value per group; their published defaults,
 # km_la's tadj = 2.3^((34 - 23) / 10)) and hd_la's per-instance vhalfl, tau
@@ -280,6 +282,7 @@ LIB_LA_GLOBALS = {
     "egl2_lr": dict(vhm=-6.9, ka=14.9, atm=1845.8, btm=-122.6, ctm=13.8, dtm=1517.74),
     "cca1_lr": dict(vhm=-43.32, ka=7.6, vhh=-58.0, ki=7.0, atm=40.0, btm=-62.5, ctm=-12.6, dtm=0.7, ath=280.0, bth=-60.7, cth=8.5, dth=19.8),
     "egl19_lr": dict(vhm=5.6, ka=7.5, vhh=24.9, ki=12.0, vhhb=-20.5, kib=8.1, ahinf=1.43, bhinf=0.14, chinf=5.96, dhinf=0.6, atm=2.9, btm=5.2, ctm=6.0, dtm=1.9, etm=1.4, ftm=30.0, gtm=2.3, ath=0.4, bth=44.6, cth=-23.0, dth=5.0, eth=36.4, fth=28.7, gth=3.7, hth=43.1),
+    "kcnl_lr": dict(kca=2e-4, a=50.0, ek_tmp=-80.0),
     "unc2_lr": dict(vhm=-12.2, ka=4.0, vhh=-52.5, ki=5.6, atm=1.5, btm=-8.2, ctm=9.1, dtm=15.4, etm=0.1, ath=83.8, bth=52.9, cth=-3.5, dth=72.1, eth=23.9, fth=-3.6),
 }
 LIB_CADYN = (dict(gamma=5e-4, decay=460.0), dict(gamma=5e-4, decay=100.0), dict(gamma=5e-4, decay=80.0))
@@ -298,7 +301,7 @@ def lib_tree_cell(seed: int, ncomp: int | None = None, nmin: int = 100, nmax: in
     The morphology is ``random_tree_cell``'s (soma, a 4-compartment axon
     initial segment, tapering dendrites).  Every compartment gets pas
     (g 3e-5, e -75); the channels of ``LIB_DENSITY`` (the user-mech set and
-    hd_la, km_la, kca_la, it2_la, kdr_la, sca_la, Ca and nine worm-lr
+    hd_la, km_la, kca_la, it2_la, kdr_la, sca_la, Ca and eleven worm-lr
     channels, with the GLOBALs of
     ``LIB_LA_GLOBALS``) go where their region's density is nonzero, scaled
     by a seeded lognormal factor (sigma 0.1);
@@ -325,9 +328,13 @@ def lib_tree_cell(seed: int, ncomp: int | None = None, nmin: int = 100, nmax: in
         gbar = d[nodes] * np.exp(0.1 * rng.standard_normal(nodes.size))
         f = {LIB_GBAR_FIELD[nm]: _f64(gbar)}
         if nm.endswith("_lr"):  # w (learned) carries the seeded factor, gb the region's density
-            f = {"w": _f64(gbar / d[nodes]), LIB_FIELDS[nm][1]: _f64(d[nodes]),
-                 LIB_FIELDS[nm][2]: _f64(np.full(nodes.size, 60.0 if LIB_FIELDS[nm][2] == "eca_tmp" else -80.0)),
-                 "dv": _f64(np.full(nodes.size, 1e-3))}
+            erev = {"eca_tmp": 60.0, "ena_tmp": 30.0}
+            f = {"w": _f64(gbar / d[nodes]), LIB_FIELDS[nm][1]: _f64(d[nodes])}
+            for k in LIB_FIELDS[nm][2:]:
+                if k.endswith("_tmp") and k not in LIB_LA_GLOBALS.get(nm, {}):
+                    f[k] = _f64(np.full(nodes.size, erev.get(k, -80.0)))
+                elif k == "dv":
+                    f[k] = _f64(np.full(nodes.size, 1e-3))
         if nm == "NaTg":
             f.update(vshifth=_f64(np.zeros(nodes.size)), vshiftm=_f64(np.zeros(nodes.size)),
                      slopeh=_f64(np.full(nodes.size, 6.0)), slopem=_f64(np.full(nodes.size, 6.0)))

@@ -67,6 +67,8 @@ typedef struct hx_ctx hx_ctx;
  *                  bhinf chinf dhinf atm btm ctm dtm etm ftm gtm ath bth cth dth
  *                  eth fth gth hth; unc2_lr: vhm ka vhh ki atm btm ctm dtm etm
  *                  ath bth cth dth eth fth); current w (gb gates (v - ek_tmp)),
+ *   HX_LIB_KCNL_LR: w, gbkcnl, dv, then its GLOBALs kca, a, ek_tmp (gate from
+ *                  cai); HX_LIB_NCA_LR: w, gbnca, ena_tmp (no gate)
  *                  w the trainable weight
  * A channel needs its ion on its node (Na: NaTg, Nap_Et2; K: Im, K_Pst,
  * K_Tst, SK_E2, SKv3_1, km_la, kca_la, kdr_la; Ca: CaDynamics_E2, Ca_HVA,
@@ -105,7 +107,9 @@ enum hx_lib_type {
     HX_LIB_CCA1_LR = 26,
     HX_LIB_EGL19_LR = 27,
     HX_LIB_UNC2_LR = 28,
-    HX_LIB_NTYPE = 29
+    HX_LIB_KCNL_LR = 29,
+    HX_LIB_NCA_LR = 30,
+    HX_LIB_NTYPE = 31
 };
 typedef struct hx_lib_table {
     int n;
@@ -222,7 +226,9 @@ enum hx_param_kind {
     HX_P_CCA1_LR_W = 42,
     HX_P_EGL19_LR_W = 43,
     HX_P_UNC2_LR_W = 44,
-    HX_P_COUNT = 45
+    HX_P_KCNL_LR_W = 45,
+    HX_P_NCA_LR_W = 46,
+    HX_P_COUNT = 47
 };
 
 /* Statistics of the execution plan built at load time. */

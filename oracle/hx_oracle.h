@@ -73,12 +73,13 @@ typedef struct hxo_net {
  *   sca_la: gbar, inactF, actF, vshift, tadj | Ca: gCabar
  *   worm-lr (shl1_lr, kvs1_lr, irk_lr, egl36_lr, shk1_lr, egl2_lr, cca1_lr,
  *   egl19_lr, unc2_lr): w, gb, ek_tmp / eca_tmp, dv, then the kinetics GLOBALs
- *   in the mechanism's order */
+ *   in the mechanism's order
+ *   kcnl_lr: w, gbkcnl, dv, kca, a, ek_tmp | nca_lr: w, gbnca, ena_tmp */
 enum {
     HXO_NA_ION = 0, HXO_K_ION, HXO_CA_ION, HXO_CADYN, HXO_CA_HVA, HXO_CA_LVAST, HXO_IM, HXO_K_PST, HXO_K_TST,
     HXO_NATG, HXO_NAP_ET2, HXO_SK_E2, HXO_SKV3_1, HXO_HD_LA, HXO_KM_LA, HXO_KCA_LA, HXO_IT2_LA, HXO_KDR_LA,
     HXO_SCA_LA, HXO_CA, HXO_SHL1_LR, HXO_KVS1_LR, HXO_IRK_LR, HXO_EGL36_LR, HXO_SHK1_LR, HXO_EGL2_LR,
-    HXO_CCA1_LR, HXO_EGL19_LR, HXO_UNC2_LR, HXO_LIB_NTYPE
+    HXO_CCA1_LR, HXO_EGL19_LR, HXO_UNC2_LR, HXO_KCNL_LR, HXO_NCA_LR, HXO_LIB_NTYPE
 };
 typedef struct hxo_lib_table {
     int n;
@@ -128,7 +129,7 @@ int hxo_forward(const hxo_group* g, double v_init, int nstep, int nprobe, const 
  * every table t in type order, its instances' states (Ca_HVA, Ca_LVAst,
  * K_Pst, K_Tst, NaTg, Nap_Et2, it2_la, sca_la, Ca: m, h; Im, SKv3_1, kdr_la: m; SK_E2: z;
  * hd_la: l; km_la, kca_la: n; shl1_lr: m, hf, hs; kvs1_lr, shk1_lr: m, h;
- * irk_lr, egl2_lr: m; egl36_lr: mf, mm, ms; cca1_lr, egl19_lr, unc2_lr: m, h;
+ * irk_lr, egl2_lr, kcnl_lr: m; egl36_lr: mf, mm, ms; cca1_lr, egl19_lr, unc2_lr: m, h;
  * ca_ion: cai)
  * appended to lib_final (nlib_final doubles available; -2 if too small). */
 int hxo_forward_lib(const hxo_group* g, double v_init, int nstep, int nprobe, const int* probe, double* trace,

@@ -23,7 +23,8 @@
  *   Ca                                   src/mech/user-mech/Ca.cu
  *   shl1_lr, kvs1_lr, irk_lr, egl36_lr,  src/mech/worm-lr-mech/<name>.cu (setparames,
  *   shk1_lr, egl2_lr, cca1_lr, egl19_lr, current, state): i = w ik_tmp; the LRDS
- *   unc2_lr (calcium: i into ica)
+ *   unc2_lr (calcium: i into ica),
+ *   kcnl_lr (gate from cai), nca_lr (no gate)
  *                                        shadow gates (m_dm, ...) never reach v and
  *                                        are not carried
  * through MechTemp's finite-difference current (mech_template.cuh:589-648)
@@ -42,9 +43,9 @@
 #define FD_EPS 0.001
 
 static const int NPAR[HXO_LIB_NTYPE] = {1, 1, 4, 4, 1, 1, 1, 1, 1, 5, 1, 2, 1, 11, 6, 5, 16, 1, 5, 1,
-                                        22, 16, 12, 9, 15, 10, 16, 29, 19};
+                                        22, 16, 12, 9, 15, 10, 16, 29, 19, 6, 3};
 static const int NST[HXO_LIB_NTYPE] = {0, 0, 0, 0, 2, 2, 1, 2, 2, 2, 2, 1, 1, 1, 1, 1, 2, 1, 2, 2,
-                                       3, 2, 1, 3, 2, 1, 2, 2, 2};
+                                       3, 2, 1, 3, 2, 1, 2, 2, 2, 1, 0};
 
 struct hxo_libstate {
     double* st[HXO_LIB_NTYPE]; /* n x NST per table */
@@ -333,7 +334,7 @@ static void worm_gates(int t, double v, const double* g, double r[6]) {
     }
 }
 
-static int is_worm(int t) { return t >= HXO_SHL1_LR && t <= HXO_UNC2_LR; }
+static int is_worm(int t) { return t >= HXO_SHL1_LR && t <= HXO_NCA_LR; }
 
 static double sk_zinf(double ca) {
     double ca_safe = ca;
@@ -416,6 +417,14 @@ static double chan_current(int t, double v, const double* p, const double* s, do
         case HXO_UNC2_LR: {
             const double ica_tmp = p[1] * s[0] * s[1] * (v - erev);
             return p[0] * ica_tmp;
+        }
+        case HXO_KCNL_LR: {
+            const double ik_tmp = p[1] * s[0] * (v - erev);
+            return p[0] * ik_tmp;
+        }
+        case HXO_NCA_LR: {
+            const double ina_tmp = p[1] * (v - erev);
+            return p[0] * ina_tmp;
         }
         default:
             return 0.0;
@@ -532,6 +541,12 @@ void hxo_lib_init(const hxo_group* g, struct hxo_libstate* L, const double* v) {
                 case HXO_SCA_LA: scala_trates(v[i] + p[3], p, g->dt, r); break;
                 case HXO_CA: ca_rates(v[i], r); break;
             }
+            if (t == HXO_KCNL_LR) { /* minf = cai / (kca + cai) */
+                const double cai = L->cai[L->ca_of[i]];
+                s[0] = cai / (p[3] + cai);
+                continue;
+            }
+            if (t == HXO_NCA_LR) continue; /* no INITIAL */
             if (is_worm(t)) { /* every gate at its steady state */
                 double wr[6] = {0, 0, 0, 0, 0, 0};
                 worm_gates(t, v[i], p + 4, wr);
@@ -561,10 +576,11 @@ void hxo_lib_current(const hxo_group* g, struct hxo_libstate* L, const double* v
             const int i = T->node[j];
             const double* p = T->par + NPAR[t] * j;
             const double* s = L->st[t] + NST[t] * j;
-            const double e = ion == 3 ? p[3] : ion == 4 ? p[2] : ion_erev(L, ion, i);
+            const double e = ion == 3 ? p[3] : t == HXO_KCNL_LR ? p[5] : ion == 4 ? p[2] : ion_erev(L, ion, i);
             double gg = chan_current(t, v[i] + 0.001, p, s, e);
             const double r = chan_current(t, v[i], p, s, e);
-            if (ion == 2 || t >= HXO_CCA1_LR) L->ica[L->ca_of[i]] += r; /* worm-lr calcium: i into ica */
+            if (ion == 2 || (t >= HXO_CCA1_LR && t <= HXO_UNC2_LR))
+                L->ica[L->ca_of[i]] += r; /* worm-lr calcium: i into ica */
             gg = (gg - r) / FD_EPS;
             rhs[i] -= r;
             d[i] += gg;
@@ -635,6 +651,13 @@ void hxo_lib_state(const hxo_group* g, struct hxo_libstate* L, const double* v) 
                 s[1] = s[1] + r[3] * (r[2] - s[1]);
                 continue;
             }
+            if (t == HXO_KCNL_LR) { /* at the state phase's cai; tm = a */
+                const double cai = L->cai[L->ca_of[i]];
+                const double inf = cai / (p[3] + cai), tau = p[4];
+                s[0] = s[0] + (1.0 - exp(dt * ((-1.0) / tau))) * (-(inf / tau) / ((-1.0) / tau) - s[0]);
+                continue;
+            }
+            if (t == HXO_NCA_LR) continue; /* no STATE */
             if (is_worm(t)) { /* x + (1 - exp(dt ((-1) / tau))) (-(inf / tau) / ((-1) / tau) - x) */
                 double wr[6] = {0, 0, 0, 0, 0, 0};
                 worm_gates(t, v[i], p + 4, wr);
