@@ -65,9 +65,11 @@ HX_P = {
     "unc2_lr.w": 44,
     "kcnl_lr.w": 45,
     "nca_lr.w": 46,
+    "kqt3_lr.w": 47,
+    "cainternm_lr.vcell": 48,
 }
-HX_P_COUNT = 47
-HX_LIB_NTYPE = 31
+HX_P_COUNT = 49
+HX_LIB_NTYPE = 33
 
 
 class LibTable(C.Structure):

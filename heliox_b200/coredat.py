@@ -89,6 +89,8 @@ LIB_MECH_TABLE: List[Tuple[int, str, int, int, int, int, int, float]] = [
     (41, "unc2_lr", 0, 0, 0, 20, 0, 0.0),
     (42, "kcnl_lr", 0, 0, 0, 16, 0, 0.0),
     (43, "nca_lr", 0, 0, 0, 9, 0, 0.0),
+    (44, "kqt3_lr", 0, 0, 0, 27, 0, 0.0),
+    (45, "cainternm_lr", 0, 0, 0, 6, 0, 0.0),
 ]
 # data column of each library field (its var_in_coredata_idx); SK_E2.zTau is
 # the GLOBAL zTau_SK_E2 of globals.dat (SK_E2.cu:65-66)
@@ -112,6 +114,8 @@ LIB_COLUMNS = {
     "unc2_lr": {"gbunc2": 0, "eca_tmp": 1, "w": 2, "dv": 3},
     "kcnl_lr": {"gbkcnl": 0, "w": 1, "dv": 2},
     "nca_lr": {"gbnca": 0, "ena_tmp": 1, "w": 2},
+    "kqt3_lr": {"gbkqt3": 0, "ek_tmp": 1, "w": 2, "dv": 3},
+    "cainternm_lr": {"vcell": 0},
 }
 # GLOBALs the loader requires of a mechanism that the dynamics do not read
 # (km_la.cu:70-80: its table parameters), written with these values

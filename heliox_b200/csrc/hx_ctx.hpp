@@ -159,7 +159,7 @@ struct hx_ctx {
     int lib_nst = 0;                // states over all entries
     hx::DevLib L{};
     DevBuf<int> lib_node_off, lib_ent, lib_ent_st, lib_ent_fix;
-    DevBuf<unsigned> lib_mask;
+    DevBuf<unsigned long long> lib_mask;
     DevBuf<double> lib_fix, lib_st, lib_lam, lib_nica, lib_nlica, lib_tape, lib_ck;
 
     // ---- a cell split across CTAs (hx_split.cu)

@@ -179,6 +179,16 @@ HXD Dual<N> pow(const Dual<N>& a, double c) {
     for (int i = 0; i < N; ++i) r.d[i] = s * a.d[i];
     return r;
 }
+template <int N>
+HXD Dual<N> exp10(const Dual<N>& a) {  // 10^a, d/da = ln(10) 10^a
+    Dual<N> r;
+    r.v = ::exp10(a.v);
+    const double s = 2.302585092994045684 * r.v;
+#pragma unroll
+    for (int i = 0; i < N; ++i) r.d[i] = s * a.d[i];
+    return r;
+}
+HXD double exp10(double x) { return ::exp10(x); }
 HXD double exp(double x) { return ::exp(x); }
 HXD double log(double x) { return ::log(x); }
 HXD double pow(double x, double c) { return ::pow(x, c); }
@@ -575,7 +585,7 @@ struct KdrLa {
     static constexpr int kS = 1, kP = 1, kIon = 1;
     static constexpr bool kCai = false;
     static constexpr int kErevFix = 0;
-    static constexpr bool kInitZero = true;
+    static constexpr unsigned kInitZero = 1u;  // bit j: gate j starts at 0
     template <class T>
     __device__ static T cur(const T& v, const T* s, const T* p, const double*, const T& e) {
         const T m2 = s[0] * s[0];
@@ -840,6 +850,64 @@ struct NcaLr : WormBase {  // nca_lr.cu: a weighted leak, f = gb, ena_tmp
     template <class T>
     __device__ static void gates(const T&, const double*, const T&, T*) {}
 };
+// kqt3_lr.cu: w (gb (0.3 mf + 0.7 ms) ww s (v - ek)) with k_ion's ek; f = gb,
+// ek_tmp (not read), dv, then the GLOBALs vhm ka vhw kiw aw bw vhs kis as bs
+// atmf btmf ctmf atms btms ctms dtms etms ftms gtms atw btw ctw dtw ats; its
+// INITIAL starts mf and ms at 0
+struct Kqt3Lr : WormBase {
+    static constexpr int kS = 4;
+    static constexpr int kIon = 1;
+    static constexpr unsigned kInitZero = 3u;
+    template <class T>
+    __device__ static T cur(const T& v, const T* s, const T* p, const double* f, const T& e) {
+        return p[0] * (f[0] * (0.3 * s[0] + 0.7 * s[1]) * s[2] * s[3] * (v - e));
+    }
+    template <class T>
+    __device__ static void gates(const T& v, const double* f, const T&, T* r) {
+        const double* g = f + 3;
+        const T minf = sig_up(v, g[0], g[1]);
+        const T uf = (v + g[11]) * rcp(g[12]);
+        const T uw = (v - g[22]) * rcp(g[23]);
+        r[0] = minf;
+        r[1] = g[10] * rcp(1.0 + uf * uf);
+        r[2] = minf;
+        r[3] = g[13] + g[14] * rcp(1.0 + exp10(-g[15] * (g[16] - v))) + g[17] * rcp(1.0 + exp10(-g[18] * (g[19] + v)));
+        r[4] = g[4] + g[5] * sig_dn(v, g[2], g[3]);
+        r[5] = g[20] + g[21] * rcp(1.0 + uw * uw);
+        r[6] = g[8] + g[9] * sig_dn(v, g[6], g[7]);
+        r[7] = T(g[24]);
+    }
+};
+
+// cainternm_lr.cu state_single_node: the calcium update c = cai_old + dt
+// alpha(c), alpha = -f ica 1e6 / (2 F vcell) - (c - caeq) / tca at or below
+// 60 mV (the drive term drops above), solved by the reference's Newton
+// iterations (F = 96485; f = f, tca, caeq).  alpha is linear in c, so the
+// iterations land on the closed form (cai_old + dt (A + caeq / tca)) /
+// (1 + dt / tca) up to rounding; the adjoint differentiates that form.
+__device__ __forceinline__ double caint_newton(double old_cai, double ica, double vcell, const double* f, double v,
+                                               double dt) {
+    const double fr = f[0], tca = f[1], caeq = f[2];
+    double c = old_cai;
+    for (int it = 0; it < 50; ++it) {
+        const double alpha = v <= 60.0 ? (-fr * ica * 1e6 / (2.0 * 96485.0 * vcell)) - ((c - caeq) / tca)
+                                       : -(c - caeq) / tca;
+        const double F = (-c + alpha * dt + old_cai) / dt;
+        const double J = (-1.0 + (-1.0 / tca) * dt) / dt;
+        const double delta = F / J;
+        c -= delta;
+        const double change = fabs(old_cai) > 1e-8 ? fabs(delta / old_cai) : fabs(delta);
+        if (change <= 1e-6 && fabs(F) <= 1e-8) break;
+    }
+    return c;
+}
+template <class T>
+__device__ __forceinline__ T caint_closed(const T& old_cai, const T& ica, const T& vcell, const double* f, double v,
+                                          double dt) {
+    const double tca = f[1], caeq = f[2];
+    const T a = v <= 60.0 ? (-f[0] * 1e6 / (2.0 * 96485.0)) * ica * rcp(vcell) : T(0.0);
+    return (old_cai + dt * (a + caeq / tca)) * (1.0 / (1.0 + dt / tca));
+}
 
 // the ion whose current a channel writes: kIonCur when it names one, else its
 // erev ion (0 Na, 1 K, 2 Ca; none for own-erev channels)
@@ -869,9 +937,9 @@ __device__ __forceinline__ T cadyn(const T& cai, const T& ica, const T& gamma, c
 enum LibType : int {
     kNaIon = 0, kKIon, kCaIon, kCaDyn, kCaHVA, kCaLVAst, kIm, kKPst, kKTst, kNaTg, kNapEt2, kSKE2, kSKv31, kHdLa,
     kKmLa, kKcaLa, kIt2La, kKdrLa, kScaLa, kCaPlain, kShl1Lr, kKvs1Lr, kIrkLr, kEgl36Lr, kShk1Lr, kEgl2Lr, kCca1Lr,
-    kEgl19Lr, kUnc2Lr, kKcnlLr, kNcaLr, kNType
+    kEgl19Lr, kUnc2Lr, kKcnlLr, kNcaLr, kKqt3Lr, kCainternmLr, kNType
 };
-static_assert(kNType <= 32, "the per-node type mask (DevLib::mask) holds one bit per type");
+static_assert(kNType <= 64, "the per-node type mask (DevLib::mask) holds one bit per type");
 // first trainable kind of each type, relative to HX_P_CADYN_GAMMA (-1: none)
 __host__ __device__ constexpr int kind0(int t) {
     return t < kCaDyn ? -1 : t == kCaDyn ? 0 : t + 0;
@@ -879,7 +947,8 @@ __host__ __device__ constexpr int kind0(int t) {
 // states per entry / fixed parameters per entry / trainable parameters per instance
 __host__ __device__ constexpr int nstate(int t) {
     return t == kCaIon ? 1
-           : t == kNcaLr ? 0
+           : (t == kNcaLr || t == kCainternmLr) ? 0
+           : t == kKqt3Lr ? 4
            : (t == kShl1Lr || t == kEgl36Lr) ? 3
            : (t == kIm || t == kSKE2 || t == kSKv31 || t == kHdLa || t == kKmLa || t == kKcaLa || t == kKdrLa ||
               t == kIrkLr || t == kEgl2Lr || t == kKcnlLr)
@@ -891,7 +960,8 @@ __host__ __device__ constexpr int nfix(int t) {
     return (t == kNaIon || t == kKIon) ? 1 : t == kCaIon ? 4 : t == kNaTg ? 4 : t == kSKE2 ? 1 : t == kHdLa ? 9
            : t == kKmLa ? 5 : t == kKcaLa ? 4 : t == kIt2La ? 15 : t == kScaLa ? 4 : t == kShl1Lr ? 21
            : t == kKvs1Lr ? 15 : t == kIrkLr ? 11 : t == kEgl36Lr ? 8 : t == kShk1Lr ? 14 : t == kEgl2Lr ? 9
-           : t == kCca1Lr ? 15 : t == kEgl19Lr ? 28 : t == kUnc2Lr ? 18 : t == kKcnlLr ? 5 : t == kNcaLr ? 2 : 0;
+           : t == kCca1Lr ? 15 : t == kEgl19Lr ? 28 : t == kUnc2Lr ? 18 : t == kKcnlLr ? 5 : t == kNcaLr ? 2
+           : t == kKqt3Lr ? 28 : t == kCainternmLr ? 3 : 0;
 }
 __host__ __device__ constexpr int ntrain(int t) { return t < kCaDyn ? 0 : t == kCaDyn ? 4 : 1; }
 
@@ -922,7 +992,8 @@ __host__ __device__ constexpr int ntrain(int t) { return t < kCaDyn ? 0 : t == k
     X(kEgl19Lr, Egl19Lr)   \
     X(kUnc2Lr, Unc2Lr)     \
     X(kKcnlLr, KcnlLr)     \
-    X(kNcaLr, NcaLr)
+    X(kNcaLr, NcaLr)       \
+    X(kKqt3Lr, Kqt3Lr)
 
 // ------------------------------------------------------------ drivers
 // one channel's forward contribution; returns I(v) (the ion current)
@@ -973,21 +1044,22 @@ __device__ __forceinline__ void chan_state(double v, double dt, double* s, const
     for (int j = 0; j < M::kS; ++j) s[j] = cnexp(s[j], r[2 * j], r[2 * j + 1], dt);
 }
 
-// INITIAL: every gate at its steady state (kdr_la: at 0)
+// INITIAL: every gate at its steady state, except the gates of the bit mask
+// kInitZero at 0 (kdr_la: m; kqt3_lr: mf, ms)
 template <class M, class = void>
 struct InitZero {
-    static constexpr bool value = false;
+    static constexpr unsigned value = 0u;
 };
 template <class M>
 struct InitZero<M, decltype((void)M::kInitZero)> {
-    static constexpr bool value = M::kInitZero;
+    static constexpr unsigned value = M::kInitZero;
 };
 template <class M>
 __device__ __forceinline__ void chan_init(double v, double* s, const double* f, double cai) {
     double r[2 * M::kS + 1];
     M::template gates<double>(v, f, cai, r);
 #pragma unroll
-    for (int j = 0; j < M::kS; ++j) s[j] = InitZero<M>::value ? 0.0 : r[2 * j];
+    for (int j = 0; j < M::kS; ++j) s[j] = ((InitZero<M>::value >> j) & 1u) ? 0.0 : r[2 * j];
 }
 
 // Adjoint of one channel's state update s_{k+1} = F(v_{k+1}, s_k[, cai_{k+1}]):
@@ -1064,7 +1136,8 @@ __device__ __forceinline__ double lib_current(const DevLib& L, int gi, double v,
 }
 
 // State phase of the nodes [i0, i1) of a cell that this thread owns (i0 +
-// tl, step nt), mechanism type by mechanism type: CaDynamics_E2 first (from
+// tl, step nt), mechanism type by mechanism type: the calcium dynamics
+// (CaDynamics_E2 or cainternm_lr) first (from
 // the step's calcium current L.nica), then the channels in type order at the
 // new voltage -- per node the reference's order (nonvint_cpu), and each pass
 // runs one mechanism's code over all the thread's nodes (shorter live
@@ -1075,12 +1148,12 @@ __device__ __forceinline__ void lib_state_type(const DevLib& L, int pb, int i0, 
                                                const double* sv) {
     for (int i = i0 + tl; i < i1; i += nt) {
         const int gi = pb + i;
-        const unsigned m = __ldg(L.mask + gi);
-        if (!(m & (1u << T))) continue;
+        const unsigned long long m = __ldg(L.mask + gi);
+        if (!(m & (1ull << T))) continue;
         const int e0 = __ldg(L.node_off + gi);
-        const int e = e0 + __popc(m & ((1u << T) - 1u));
+        const int e = e0 + __popcll(m & ((1ull << T) - 1ull));
         double cai = 0.0;
-        if (M::kCai) cai = L.st[__ldg(L.ent_st + e0 + __popc(m & ((1u << kCaIon) - 1u)))];
+        if (M::kCai) cai = L.st[__ldg(L.ent_st + e0 + __popcll(m & ((1ull << kCaIon) - 1ull)))];
         chan_state<M>(sv[i], L.dt, L.st + __ldg(L.ent_st + e), L.fix + __ldg(L.ent_fix + e), cai);
     }
 }
@@ -1089,13 +1162,21 @@ __device__ __forceinline__ void lib_state_cell(const DevLib& L, int pb, int i0, 
                                                const double* sv) {
     for (int i = i0 + tl; i < i1; i += nt) {
         const int gi = pb + i;
-        const unsigned m = __ldg(L.mask + gi);
-        if (!(m & (1u << kCaDyn))) continue;
-        const int e = __ldg(L.node_off + gi) + __popc(m & ((1u << kCaDyn) - 1u));
-        const int inst = entry_inst(__ldg(L.ent + e));
-        double* cai = L.st + __ldg(L.ent_st + e - 1);  // the node's ca_ion entry precedes CaDynamics_E2
-        *cai = cadyn<double>(*cai, L.nica[gi], __ldg(L.prm[0] + inst), __ldg(L.prm[1] + inst),
-                             __ldg(L.prm[2] + inst), __ldg(L.prm[3] + inst), L.dt);
+        const unsigned long long m = __ldg(L.mask + gi);
+        if (m & (1ull << kCaDyn)) {
+            const int e = __ldg(L.node_off + gi) + __popcll(m & ((1ull << kCaDyn) - 1ull));
+            const int inst = entry_inst(__ldg(L.ent + e));
+            double* cai = L.st + __ldg(L.ent_st + e - 1);  // the node's ca_ion entry precedes CaDynamics_E2
+            *cai = cadyn<double>(*cai, L.nica[gi], __ldg(L.prm[0] + inst), __ldg(L.prm[1] + inst),
+                                 __ldg(L.prm[2] + inst), __ldg(L.prm[3] + inst), L.dt);
+        } else if (m & (1ull << kCainternmLr)) {
+            const int e0 = __ldg(L.node_off + gi);
+            const int e = e0 + __popcll(m & ((1ull << kCainternmLr) - 1ull));
+            const int inst = entry_inst(__ldg(L.ent + e));
+            double* cai = L.st + __ldg(L.ent_st + e0 + __popcll(m & ((1ull << kCaIon) - 1ull)));
+            *cai = caint_newton(*cai, L.nica[gi], __ldg(L.prm[kind0(kCainternmLr)] + inst), L.fix + __ldg(L.ent_fix + e),
+                                sv[i], L.dt);
+        }
     }
 #define HX_LIB_STT(T_, M_) lib_state_type<T_, M_>(L, pb, i0, i1, tl, nt, sv);
     HX_LIB_CHANNELS(HX_LIB_STT)
@@ -1144,6 +1225,7 @@ __device__ __forceinline__ double lib_state_adj(const DevLib& L, int gi, double 
     double* lam = L.lam;
     double mu = 0.0, lcai1 = 0.0;
     bool dyn = false;
+    int ci = -1;  // the cainternm_lr entry: last in type order, applied first in the state phase
     for (int e = e1 - 1; e >= e0; --e) {
         const int code = __ldg(L.ent + e), t = entry_type(code), inst = entry_inst(code);
         const int so = __ldg(L.ent_st + e);
@@ -1167,6 +1249,10 @@ __device__ __forceinline__ double lib_state_adj(const DevLib& L, int gi, double 
 #pragma unroll
                 for (int j = 0; j < 4; ++j) L.grad[j][inst] += lt * out.d[2 + j];
             } break;
+            case kCainternmLr:
+                dyn = true;
+                ci = e;
+                break;
             case kCaIon:
                 if (!dyn) {  // no calcium dynamics: cai_{k+1} = cai_k
                     lam[cs] += lcai1;
@@ -1176,6 +1262,17 @@ __device__ __forceinline__ double lib_state_adj(const DevLib& L, int gi, double 
             default:
                 break;
         }
+    }
+    if (ci >= 0) {  // after every reader of cai_{k+1} has added to lcai1
+        using D = Dual<3>;
+        const int inst = entry_inst(__ldg(L.ent + ci));
+        const double lt = lam[cs] + lcai1;
+        const D out = caint_closed<D>(D::var(Xk[cs], 0), D::var(ica, 1),
+                                      D::var(__ldg(L.prm[kind0(kCainternmLr)] + inst), 2),
+                                      L.fix + __ldg(L.ent_fix + ci), v1, L.dt);
+        lam[cs] = lt * out.d[0];
+        L.nlica[gi] = lt * out.d[1];
+        L.grad[kind0(kCainternmLr)][inst] += lt * out.d[2];
     }
     return mu;
 }

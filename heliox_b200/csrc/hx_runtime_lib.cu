@@ -1,6 +1,6 @@
 // hx_runtime_lib.cu -- host side of the library mechanisms (hx_lib.cuh):
 // the per-node entry tables in GPU order, the parameter kinds
-// HX_P_CADYN_GAMMA .. HX_P_NCA_LR_W, and the device arrays of DevLib.
+// HX_P_CADYN_GAMMA .. HX_P_CAINTERNM_LR_VCELL, and the device arrays of DevLib.
 //
 // The reference keeps one instance table per mechanism type
 // (MechTemp::reg_node_indices / read_data_from_coredat,
@@ -32,7 +32,8 @@ const char* kTypeName[HX_LIB_NTYPE] = {"na_ion", "k_ion", "ca_ion",  "CaDynamics
                                        "Nap_Et2", "SK_E2", "SKv3_1", "hd_la",         "km_la",
                                        "kca_la", "it2_la", "kdr_la", "sca_la",        "Ca",
                                        "shl1_lr", "kvs1_lr", "irk_lr", "egl36_lr",    "shk1_lr",
-                                       "egl2_lr", "cca1_lr", "egl19_lr", "unc2_lr", "kcnl_lr", "nca_lr"};
+                                       "egl2_lr", "cca1_lr", "egl19_lr", "unc2_lr", "kcnl_lr", "nca_lr",
+                                       "kqt3_lr", "cainternm_lr"};
 
 // columns of a type's hx_lib_table rows (trainable first, then fixed); hd_la's
 // GLOBALs q10 and qtl enter the device's fixed parameters as one factor
@@ -56,6 +57,7 @@ int ions_needed(int t) {
         case HX_LIB_EGL36_LR:
         case HX_LIB_SHK1_LR:
         case HX_LIB_EGL2_LR:
+        case HX_LIB_KQT3_LR:
             return 2;
         case HX_LIB_SK_E2:
         case HX_LIB_KCA_LA:
@@ -71,6 +73,7 @@ int ions_needed(int t) {
         case HX_LIB_UNC2_LR:
             return 4;
         case HX_LIB_CADYN:
+        case HX_LIB_CAINTERNM_LR:
         case HX_LIB_CA_HVA:
         case HX_LIB_CA_LVAST:
             return 4;
@@ -82,7 +85,7 @@ int ions_needed(int t) {
 
 int hx_lib_type_of_kind(int kind) {
     if (kind >= HX_P_CADYN_GAMMA && kind <= HX_P_CADYN_MINCAI) return HX_LIB_CADYN;
-    if (kind >= HX_P_CA_HVA_G && kind <= HX_P_NCA_LR_W) return kind - HX_P_CA_HVA_G + HX_LIB_CA_HVA;
+    if (kind >= HX_P_CA_HVA_G && kind < HX_P_COUNT) return kind - HX_P_CA_HVA_G + HX_LIB_CA_HVA;
     return -1;
 }
 
@@ -104,7 +107,7 @@ int hx_lib_load(hx_ctx* ctx, const hx_group_desc* desc) {
         }
     cudaStream_t st = ctx->st;
     if (!any) {
-        for (int k = HX_P_CADYN_GAMMA; k <= HX_P_NCA_LR_W; k++) {
+        for (int k = HX_P_CADYN_GAMMA; k < HX_P_COUNT; k++) {
             ctx->kmap_h[k].assign(1, 0);
             HXC(ctx->kmap[k].upload(ctx->kmap_h[k], st));
             HXC(ctx->prm[k].ensure(1));
@@ -139,15 +142,18 @@ int hx_lib_load(hx_ctx* ctx, const hx_group_desc* desc) {
     }
     for (int j = 0; j < D->t[HX_LIB_CA_ION].n; j++)
         if (!(D->t[HX_LIB_CA_ION].par[4 * j] > 0.0)) return fail(ctx, "ca_ion: cai must be positive");
+    for (int j = 0; j < D->t[HX_LIB_CAINTERNM_LR].n; j++)
+        if (at[HX_LIB_CADYN][D->t[HX_LIB_CAINTERNM_LR].node[j]] >= 0)
+            return fail(ctx, "CaDynamics_E2 and cainternm_lr on one node: one calcium dynamics per node");
     // entries in GPU node order, types ascending on a node
     std::vector<int> node_off(nn + 1, 0), ent, ent_st, ent_fix;
-    std::vector<unsigned> mask(std::max(nn, 1), 0);
+    std::vector<unsigned long long> mask(std::max(nn, 1), 0);
     std::vector<double> fix;
     std::vector<std::map<std::vector<double>, int>> fix_of(HX_LIB_NTYPE);
     std::vector<int> inst(HX_LIB_NTYPE, 0);
     std::vector<std::vector<double>> prm(hx::kLibKinds);
     for (int k = 0; k < hx::kLibKinds; k++) prm[k].assign(1, 0.0);
-    for (int k = HX_P_CADYN_GAMMA; k <= HX_P_NCA_LR_W; k++)
+    for (int k = HX_P_CADYN_GAMMA; k < HX_P_COUNT; k++)
         ctx->kmap_h[k].assign(std::max(ctx->lib_n[hx_lib_type_of_kind(k)], 1), 0);
     int nst = 0;
     for (int gi = 0; gi < nn; gi++) {
@@ -158,7 +164,7 @@ int hx_lib_load(hx_ctx* ctx, const hx_group_desc* desc) {
             const int ntr = L::ntrain(t), nfx = L::nfix(t), q = inst[t]++;
             const double* par = D->t[t].par + (size_t)desc_cols(t) * j;
             ent.push_back(t << 24 | q);
-            mask[gi] |= 1u << t;
+            mask[gi] |= 1ull << t;
             ent_st.push_back(nst);
             nst += L::nstate(t);
             std::vector<double> fv;
@@ -193,12 +199,12 @@ int hx_lib_load(hx_ctx* ctx, const hx_group_desc* desc) {
     if (fix.empty()) fix.push_back(0.0);
     if (ent.empty()) ent.push_back(0);
     // GLOBALs of a mechanism: one value over its instances
-    const int glo_t[16] = {HX_LIB_SK_E2,    HX_LIB_HD_LA,    HX_LIB_KM_LA,   HX_LIB_KCA_LA,   HX_LIB_IT2_LA,
+    const int glo_t[18] = {HX_LIB_SK_E2,    HX_LIB_HD_LA,    HX_LIB_KM_LA,   HX_LIB_KCA_LA,   HX_LIB_IT2_LA,
                            HX_LIB_SCA_LA,   HX_LIB_SHL1_LR,  HX_LIB_KVS1_LR, HX_LIB_IRK_LR,   HX_LIB_EGL36_LR,
                            HX_LIB_SHK1_LR,  HX_LIB_EGL2_LR,  HX_LIB_CCA1_LR, HX_LIB_EGL19_LR, HX_LIB_UNC2_LR,
-                           HX_LIB_KCNL_LR};
-    const int glo_c0[16] = {1, 3, 1, 1, 1, 3, 4, 4, 4, 4, 4, 4, 4, 4, 4, 3};
-    for (int u = 0; u < 16; u++) {
+                           HX_LIB_KCNL_LR,  HX_LIB_KQT3_LR,  HX_LIB_CAINTERNM_LR};
+    const int glo_c0[18] = {1, 3, 1, 1, 1, 3, 4, 4, 4, 4, 4, 4, 4, 4, 4, 3, 4, 1};
+    for (int u = 0; u < 18; u++) {
         const hx_lib_table& T = D->t[glo_t[u]];
         const int nc = desc_cols(glo_t[u]);
         for (int j = 1; j < T.n; j++)
@@ -213,7 +219,7 @@ int hx_lib_load(hx_ctx* ctx, const hx_group_desc* desc) {
     HXC(ctx->lib_ent_st.upload(ent_st, st));
     HXC(ctx->lib_ent_fix.upload(ent_fix, st));
     HXC(ctx->lib_fix.upload(fix, st));
-    for (int k = HX_P_CADYN_GAMMA; k <= HX_P_NCA_LR_W; k++) {
+    for (int k = HX_P_CADYN_GAMMA; k < HX_P_COUNT; k++) {
         HXC(ctx->kmap[k].upload(ctx->kmap_h[k], st));
         HXC(ctx->prm[k].upload(prm[k - HX_P_CADYN_GAMMA], st));
     }

@@ -68,6 +68,7 @@ SPIKE_THRESHOLD = 10.0
 # var_in_coredata_idx); ion fields follow eion.cuh:81-86 (cai is the initial
 # concentration, ifields['nernst'] = 1 recomputes eca from cai/cao every step,
 # eion.cuh:155-166).  na_ion / k_ion on an hh node must carry hh's ena / ek.
+KQT3_GLOBALS = ("vhm", "ka", "vhw", "kiw", "aw", "bw", "vhs", "kis", "as", "bs", "atmf", "btmf", "ctmf", "atms", "btms", "ctms", "dtms", "etms", "ftms", "gtms", "atw", "btw", "ctw", "dtw", "ats")
 LIB_MECHS = (
     ("na_ion", ("ena",), 0),
     ("k_ion", ("ek",), 0),
@@ -103,6 +104,10 @@ LIB_MECHS = (
     ("unc2_lr", ("w", "gbunc2", "eca_tmp", "dv", "vhm", "ka", "vhh", "ki", "atm", "btm", "ctm", "dtm", "etm", "ath", "bth", "cth", "dth", "eth", "fth"), 1),
     ("kcnl_lr", ("w", "gbkcnl", "dv", "kca", "a", "ek_tmp"), 1),
     ("nca_lr", ("w", "gbnca", "ena_tmp"), 1),
+    # kqt3_lr: w (gb (0.3 mf + 0.7 ms) ww s (v - ek)) with k_ion's ek; ek_tmp is carried, not read
+    ("kqt3_lr", ("w", "gbkqt3", "ek_tmp", "dv") + KQT3_GLOBALS, 1),
+    # cainternm_lr (calcium dynamics of the worm-lr set): vcell per instance, GLOBALs f, tca, caeq
+    ("cainternm_lr", ("vcell", "f", "tca", "caeq"), 1),
 )
 # fields that are GLOBALs of their mechanism in the reference (one value per
 # group, written to globals.dat as <field>_<mechanism>)
@@ -124,6 +129,8 @@ LIB_GLOBALS = {
     "egl19_lr": ("vhm", "ka", "vhh", "ki", "vhhb", "kib", "ahinf", "bhinf", "chinf", "dhinf", "atm", "btm", "ctm", "dtm", "etm", "ftm", "gtm", "ath", "bth", "cth", "dth", "eth", "fth", "gth", "hth",),
     "unc2_lr": ("vhm", "ka", "vhh", "ki", "atm", "btm", "ctm", "dtm", "etm", "ath", "bth", "cth", "dth", "eth", "fth",),
     "kcnl_lr": ("kca", "a", "ek_tmp"),
+    "kqt3_lr": KQT3_GLOBALS,
+    "cainternm_lr": ("f", "tca", "caeq"),
 }
 LIB_NAMES = tuple(m[0] for m in LIB_MECHS)
 LIB_FIELDS = {m[0]: m[1] for m in LIB_MECHS}
@@ -145,6 +152,8 @@ LIB_IONS = {
     "unc2_lr": ("ca",),
     "kcnl_lr": ("k", "ca"),
     "nca_lr": ("na",),
+    "kqt3_lr": ("k",),
+    "cainternm_lr": ("ca",),
 }
 
 
@@ -338,6 +347,9 @@ class CellGroup:
                 it = self.lib.get(ion + "_ion")
                 if it is None or not np.all(np.isin(tab.nodes, it.nodes)):
                     raise ValueError(f"{nm} needs {ion}_ion on each of its nodes")
+        cad, cin = self.lib.get("CaDynamics_E2"), self.lib.get("cainternm_lr")
+        if cad is not None and cin is not None and np.intersect1d(cad.nodes, cin.nodes).size:
+            raise ValueError("CaDynamics_E2 and cainternm_lr on one node: one calcium dynamics per node")
         for ion, key in (("na_ion", "ena"), ("k_ion", "ek")):
             it = self.lib.get(ion)
             if it is None or not it.n or not self.hh.n:
@@ -430,6 +442,7 @@ LIB_STATES = {"ca_ion": ("cai",), "Ca_HVA": ("m", "h"), "Ca_LVAst": ("m", "h"), 
               "egl19_lr": ("m", "h"),
               "unc2_lr": ("m", "h"),
               "kcnl_lr": ("m",),
+              "kqt3_lr": ("mf", "ms", "ww", "s"),
 }
 
 

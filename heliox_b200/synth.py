@@ -260,6 +260,7 @@ LIB_DENSITY = {
     "unc2_lr": (0.0, 0.0, 1e-5),
     "kcnl_lr": (1e-4, 0.0, 1e-5),
     "nca_lr": (0.0, 0.0, 2e-6),
+    "kqt3_lr": (2e-4, 0.0, 5e-5),
 }
 # GLOBALs of hd_la / km_la (one value per group; their published defaults,
 # km_la's tadj = 2.3^((34 - 23) / 10)) and hd_la's per-instance vhalfl, tau
@@ -283,9 +284,15 @@ LIB_LA_GLOBALS = {
     "cca1_lr": dict(vhm=-43.32, ka=7.6, vhh=-58.0, ki=7.0, atm=40.0, btm=-62.5, ctm=-12.6, dtm=0.7, ath=280.0, bth=-60.7, cth=8.5, dth=19.8),
     "egl19_lr": dict(vhm=5.6, ka=7.5, vhh=24.9, ki=12.0, vhhb=-20.5, kib=8.1, ahinf=1.43, bhinf=0.14, chinf=5.96, dhinf=0.6, atm=2.9, btm=5.2, ctm=6.0, dtm=1.9, etm=1.4, ftm=30.0, gtm=2.3, ath=0.4, bth=44.6, cth=-23.0, dth=5.0, eth=36.4, fth=28.7, gth=3.7, hth=43.1),
     "kcnl_lr": dict(kca=2e-4, a=50.0, ek_tmp=-80.0),
+    "kqt3_lr": dict(vhm=-12.8, ka=15.8, vhw=-1.1, kiw=28.8, aw=0.5, bw=0.5, vhs=-45.3, kis=12.3, bs=0.7,
+                    atmf=395.3, btmf=38.1, ctmf=33.59, atms=5503.0, btms=-5345.4, ctms=0.02827, dtms=-23.9,
+                    etms=-4590.6, ftms=0.0357, gtms=14.2, atw=0.5, btw=2.9, ctw=-48.09, dtw=48.83, ats=500.0,
+                    **{"as": 0.3}),
     "unc2_lr": dict(vhm=-12.2, ka=4.0, vhh=-52.5, ki=5.6, atm=1.5, btm=-8.2, ctm=9.1, dtm=15.4, etm=0.1, ath=83.8, bth=52.9, cth=-3.5, dth=72.1, eth=23.9, fth=-3.6),
 }
 LIB_CADYN = (dict(gamma=5e-4, decay=460.0), dict(gamma=5e-4, decay=100.0), dict(gamma=5e-4, decay=80.0))
+# cainternm_lr (the worm-lr calcium dynamics): vcell per instance, GLOBALs f, tca (ms), caeq (mM)
+LIB_CAINTERNM = dict(vcell=31.16, f=0.05, tca=50.0, caeq=5e-5)
 LIB_GBAR_FIELD = {nm: LIB_FIELDS[nm][0] for nm in LIB_DENSITY}
 
 
@@ -295,7 +302,7 @@ LIB_BBP_CHANNELS = ("NaTg", "Nap_Et2", "K_Pst", "K_Tst", "SKv3_1", "SK_E2", "Im"
 
 
 def lib_tree_cell(seed: int, ncomp: int | None = None, nmin: int = 100, nmax: int = 400,
-                  amp: float | None = None, channels=None) -> CellGroup:
+                  amp: float | None = None, channels=None, cadyn: str = "CaDynamics_E2") -> CellGroup:
     """One seeded random-tree cell carrying the user-mech channel set.
 
     The morphology is ``random_tree_cell``'s (soma, a 4-compartment axon
@@ -311,6 +318,8 @@ def lib_tree_cell(seed: int, ncomp: int | None = None, nmin: int = 100, nmax: in
     step).  IClamp at the soma, del 5 ms, dur 50 ms, amplitude U[0.2, 1] nA.
     celsius 34 (the channels' temperature: their rate factors hard-code it).
     ``channels``: the subset of ``LIB_DENSITY`` to place (default: all).
+    ``cadyn``: the calcium dynamics on the calcium nodes, CaDynamics_E2 or
+    cainternm_lr (``LIB_CAINTERNM``, vcell times a seeded lognormal factor).
     """
     rng = np.random.default_rng(seed + 7_000_000)
     base = random_tree_cell(seed, ncomp=ncomp, nmin=nmin, nmax=nmax, amp=amp)
@@ -350,10 +359,18 @@ def lib_tree_cell(seed: int, ncomp: int | None = None, nmin: int = 100, nmax: in
         for ion in LIB_IONS[nm]:
             need[ion][nodes] = True
     ca_nodes = np.nonzero(need["ca"])[0]
-    cad = [LIB_CADYN[r] for r in region[ca_nodes]]
-    lib["CaDynamics_E2"] = MechTable(_i32(ca_nodes), {
-        "gamma": _f64([c["gamma"] for c in cad]), "decay": _f64([c["decay"] for c in cad]),
-        "depth": _f64(np.full(ca_nodes.size, 0.1)), "minCai": _f64(np.full(ca_nodes.size, 1e-4))})
+    if cadyn == "cainternm_lr":
+        ci = LIB_CAINTERNM
+        lib["cainternm_lr"] = MechTable(_i32(ca_nodes), {
+            "vcell": _f64(ci["vcell"] * np.exp(0.1 * rng.standard_normal(ca_nodes.size))),
+            **{k: _f64(np.full(ca_nodes.size, ci[k])) for k in ("f", "tca", "caeq")}})
+    elif cadyn == "CaDynamics_E2":
+        cad = [LIB_CADYN[r] for r in region[ca_nodes]]
+        lib["CaDynamics_E2"] = MechTable(_i32(ca_nodes), {
+            "gamma": _f64([c["gamma"] for c in cad]), "decay": _f64([c["decay"] for c in cad]),
+            "depth": _f64(np.full(ca_nodes.size, 0.1)), "minCai": _f64(np.full(ca_nodes.size, 1e-4))})
+    else:
+        raise ValueError(f"unknown calcium dynamics {cadyn!r}")
     na = np.nonzero(need["na"])[0]
     k = np.nonzero(need["k"])[0]
     lib["na_ion"] = MechTable(_i32(na), {"ena": _f64(np.full(na.size, 50.0))})

@@ -20,7 +20,7 @@
 extern "C" {
 #endif
 
-#define HX_ABI_VERSION 3
+#define HX_ABI_VERSION 4
 
 typedef struct hx_ctx hx_ctx;
 
@@ -70,6 +70,13 @@ typedef struct hx_ctx hx_ctx;
  *   HX_LIB_KCNL_LR: w, gbkcnl, dv, then its GLOBALs kca, a, ek_tmp (gate from
  *                  cai); HX_LIB_NCA_LR: w, gbnca, ena_tmp (no gate)
  *                  w the trainable weight
+ *   HX_LIB_KQT3_LR (kqt3_lr.cu): w, gbkqt3, ek_tmp (carried, not read: the
+ *                  current uses k_ion's ek), dv, then its GLOBALs vhm ka vhw
+ *                  kiw aw bw vhs kis as bs atmf btmf ctmf atms btms ctms dtms
+ *                  etms ftms gtms atw btw ctw dtw ats
+ *   HX_LIB_CAINTERNM_LR (cainternm_lr.cu): vcell, then its GLOBALs f, tca,
+ *                  caeq; calcium dynamics (writes cai in the state phase), at
+ *                  most one of it and HX_LIB_CADYN per node
  * A channel needs its ion on its node (Na: NaTg, Nap_Et2; K: Im, K_Pst,
  * K_Tst, SK_E2, SKv3_1, km_la, kca_la, kdr_la; Ca: CaDynamics_E2, Ca_HVA,
  * Ca_LVAst, it2_la, sca_la, Ca, SK_E2 and kca_la (cai)); the worm-lr
@@ -109,7 +116,9 @@ enum hx_lib_type {
     HX_LIB_UNC2_LR = 28,
     HX_LIB_KCNL_LR = 29,
     HX_LIB_NCA_LR = 30,
-    HX_LIB_NTYPE = 31
+    HX_LIB_KQT3_LR = 31,
+    HX_LIB_CAINTERNM_LR = 32,
+    HX_LIB_NTYPE = 33
 };
 typedef struct hx_lib_table {
     int n;
@@ -228,7 +237,9 @@ enum hx_param_kind {
     HX_P_UNC2_LR_W = 44,
     HX_P_KCNL_LR_W = 45,
     HX_P_NCA_LR_W = 46,
-    HX_P_COUNT = 47
+    HX_P_KQT3_LR_W = 47,
+    HX_P_CAINTERNM_LR_VCELL = 48, /* cainternm_lr: vcell per instance */
+    HX_P_COUNT = 49
 };
 
 /* Statistics of the execution plan built at load time. */

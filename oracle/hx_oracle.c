@@ -707,7 +707,7 @@ static void solve_serial_T(const hxo_group* g, double* d, double* rhs) {
 /* nonvint_cpu, simulate.cpp:784-852: states at the updated v */
 static void nonvint(const hxo_group* g, hxo_state* s) {
     const double dt = g->dt;
-    hxo_lib_state_ion(g, s->lib); /* mech_write_state_ion_list first */
+    hxo_lib_state_ion(g, s->lib, s->v); /* mech_write_state_ion_list first */
     hxo_lib_state(g, s->lib, s->v);
     for (int j = 0; j < g->nhh; j++) {
         hh_rates_t r;

@@ -24,9 +24,12 @@
  *   shl1_lr, kvs1_lr, irk_lr, egl36_lr,  src/mech/worm-lr-mech/<name>.cu (setparames,
  *   shk1_lr, egl2_lr, cca1_lr, egl19_lr, current, state): i = w ik_tmp; the LRDS
  *   unc2_lr (calcium: i into ica),
- *   kcnl_lr (gate from cai), nca_lr (no gate)
+ *   kcnl_lr (gate from cai), nca_lr (no gate),
+ *   kqt3_lr (k_ion's ek; mf, ms start at 0)
  *                                        shadow gates (m_dm, ...) never reach v and
  *                                        are not carried
+ *   cainternm_lr                         src/mech/worm-lr-mech/cainternm_lr.cu (Newton
+ *                                        solve of the implicit calcium update)
  * through MechTemp's finite-difference current (mech_template.cuh:589-648)
  * and the state phase order of nonvint_cpu (simulate.cpp:784-852: mechanisms
  * that write an ion in their state update first, then the others in type
@@ -43,9 +46,9 @@
 #define FD_EPS 0.001
 
 static const int NPAR[HXO_LIB_NTYPE] = {1, 1, 4, 4, 1, 1, 1, 1, 1, 5, 1, 2, 1, 11, 6, 5, 16, 1, 5, 1,
-                                        22, 16, 12, 9, 15, 10, 16, 29, 19, 6, 3};
+                                        22, 16, 12, 9, 15, 10, 16, 29, 19, 6, 3, 29, 4};
 static const int NST[HXO_LIB_NTYPE] = {0, 0, 0, 0, 2, 2, 1, 2, 2, 2, 2, 1, 1, 1, 1, 1, 2, 1, 2, 2,
-                                       3, 2, 1, 3, 2, 1, 2, 2, 2, 1, 0};
+                                       3, 2, 1, 3, 2, 1, 2, 2, 2, 1, 0, 4, 0};
 
 struct hxo_libstate {
     double* st[HXO_LIB_NTYPE]; /* n x NST per table */
@@ -261,7 +264,7 @@ static void ca_rates(double volt, double r[4]) {
 
 /* worm-lr setparames at v: r = inf0, tau0, inf1, tau1, inf2, tau2 (the
  * time constants the cnexp update uses).  g = the GLOBALs (p + 4). */
-static void worm_gates(int t, double v, const double* g, double r[6]) {
+static void worm_gates(int t, double v, const double* g, double r[8]) {
     switch (t) {
         case HXO_SHL1_LR: { /* vhm ka vhh ki atm btm ctm dtm etm ftm athf bthf cthf dthf aths bths cths dths */
             const double minf = 1.0 / (1.0 + exp(-(v - g[0]) / g[1]));
@@ -331,10 +334,24 @@ static void worm_gates(int t, double v, const double* g, double r[6]) {
             r[3] = g[9] / (1.0 + exp(-(v - g[10]) / g[11])) + g[12] / (1.0 + exp((v - g[13]) / g[14]));
             break;
         }
+        case HXO_KQT3_LR: { /* vhm ka vhw kiw aw bw vhs kis as bs atmf btmf ctmf atms btms ctms dtms etms ftms
+                               gtms atw btw ctw dtw ats; gates mf, ms (both minf), ww, s */
+            const double minf = 1.0 / (1.0 + exp(-(v - g[0]) / g[1]));
+            r[0] = minf;
+            r[1] = g[10] / (1.0 + pow((v + g[11]) / g[12], 2.0));
+            r[2] = minf;
+            r[3] = g[13] + g[14] / (1.0 + pow(10.0, -g[15] * (g[16] - v))) +
+                   g[17] / (1.0 + pow(10.0, -g[18] * (g[19] + v)));
+            r[4] = g[4] + g[5] / (1.0 + exp((v - g[2]) / g[3]));
+            r[5] = g[20] + g[21] / (1.0 + pow((v - g[22]) / g[23], 2.0));
+            r[6] = g[8] + g[9] / (1.0 + exp((v - g[6]) / g[7]));
+            r[7] = g[24];
+            break;
+        }
     }
 }
 
-static int is_worm(int t) { return t >= HXO_SHL1_LR && t <= HXO_NCA_LR; }
+static int is_worm(int t) { return (t >= HXO_SHL1_LR && t <= HXO_NCA_LR) || t == HXO_KQT3_LR; }
 
 static double sk_zinf(double ca) {
     double ca_safe = ca;
@@ -426,6 +443,10 @@ static double chan_current(int t, double v, const double* p, const double* s, do
             const double ina_tmp = p[1] * (v - erev);
             return p[0] * ina_tmp;
         }
+        case HXO_KQT3_LR: {
+            const double ik_tmp = p[1] * (0.3 * s[0] + 0.7 * s[1]) * s[2] * s[3] * (v - erev);
+            return p[0] * ik_tmp;
+        }
         default:
             return 0.0;
     }
@@ -433,8 +454,10 @@ static double chan_current(int t, double v, const double* p, const double* s, do
 
 /* 0: na, 1: k, 2: ca (the ion whose erev a channel reads and current it writes),
  * 3: none (hd_la: its own reversal potential ehd, no ion current), 4: its own
- * reversal potential ek_tmp (the worm-lr channels; their k current is not read) */
+ * reversal potential ek_tmp (the worm-lr channels; their k current is not read;
+ * kqt3_lr reads k_ion's ek) */
 static int chan_ion(int t) {
+    if (t == HXO_KQT3_LR) return 1;
     if (is_worm(t)) return 4;
     switch (t) {
         case HXO_HD_LA:
@@ -546,11 +569,11 @@ void hxo_lib_init(const hxo_group* g, struct hxo_libstate* L, const double* v) {
                 s[0] = cai / (p[3] + cai);
                 continue;
             }
-            if (t == HXO_NCA_LR) continue; /* no INITIAL */
-            if (is_worm(t)) { /* every gate at its steady state */
-                double wr[6] = {0, 0, 0, 0, 0, 0};
+            if (t == HXO_NCA_LR || t == HXO_CAINTERNM_LR) continue; /* no INITIAL of a state */
+            if (is_worm(t)) { /* every gate at its steady state (kqt3_lr: mf = ms = 0) */
+                double wr[8] = {0, 0, 0, 0, 0, 0, 0, 0};
                 worm_gates(t, v[i], p + 4, wr);
-                for (int q = 0; q < NST[t]; q++) s[q] = wr[2 * q];
+                for (int q = 0; q < NST[t]; q++) s[q] = (t == HXO_KQT3_LR && q < 2) ? 0.0 : wr[2 * q];
                 continue;
             }
             s[0] = r[0];
@@ -572,6 +595,7 @@ void hxo_lib_current(const hxo_group* g, struct hxo_libstate* L, const double* v
     for (int t = HXO_CA_HVA; t < HXO_LIB_NTYPE; t++) {
         const hxo_lib_table* T = &lib->t[t];
         const int ion = chan_ion(t);
+        if (t == HXO_CAINTERNM_LR) continue; /* no current */
         for (int j = 0; j < T->n; j++) {
             const int i = T->node[j];
             const double* p = T->par + NPAR[t] * j;
@@ -589,8 +613,8 @@ void hxo_lib_current(const hxo_group* g, struct hxo_libstate* L, const double* v
 }
 
 /* state phase, part 1: mechanisms that write an ion in their state update
- * (CaDynamics_E2) */
-void hxo_lib_state_ion(const hxo_group* g, struct hxo_libstate* L) {
+ * (CaDynamics_E2, then cainternm_lr), in type order */
+void hxo_lib_state_ion(const hxo_group* g, struct hxo_libstate* L, const double* v) {
     if (!L) return;
     const hxo_lib_table* T = &g->lib->t[HXO_CADYN];
     const double dt = g->dt;
@@ -604,6 +628,33 @@ void hxo_lib_state_ion(const hxo_group* g, struct hxo_libstate* L) {
         const double exp_factor = exp(dt * (-1.0 / decay_val));
         const double steady_term = -(drive_ica - (-minCai_val) / decay_val) / (-1.0 / decay_val);
         L->cai[c] = cai_val + (1.0 - exp_factor) * (steady_term - cai_val);
+    }
+    /* cainternm_lr.cu state_single_node: Newton iterations on
+     * F(c) = (-c + alpha(c) dt + cai_old) / dt, alpha = -f ica 1e6 / (2 F vcell)
+     * - (c - caeq) / tca below 60 mV, -(c - caeq) / tca above; p = vcell, f,
+     * tca, caeq */
+    const hxo_lib_table* C = &g->lib->t[HXO_CAINTERNM_LR];
+    for (int j = 0; j < C->n; j++) {
+        const int i = C->node[j], c = L->ca_of[i];
+        const double* p = C->par + 4 * j;
+        const double FARADAY = 96485.0;
+        const double ica = L->ica[c], old_cai = L->cai[c];
+        double current_cai = old_cai;
+        for (int iter = 0; iter < 50; iter++) {
+            double alpha_val;
+            if (v[i] <= 60.0)
+                alpha_val = (-p[1] * ica * pow(10.0, 6.0) / (2.0 * FARADAY * p[0])) - ((current_cai - p[3]) / p[2]);
+            else
+                alpha_val = -(current_cai - p[3]) / p[2];
+            const double F = (-current_cai + alpha_val * dt + old_cai) / dt;
+            const double dalpha_dcai = -1.0 / p[2];
+            const double J = (-1.0 + dalpha_dcai * dt) / dt;
+            const double delta = F / J;
+            current_cai -= delta;
+            const double change = (fabs(old_cai) > 1e-8) ? fabs(delta / old_cai) : fabs(delta);
+            if (change <= 1e-6 && fabs(F) <= 1e-8) break;
+        }
+        L->cai[c] = current_cai;
     }
 }
 
@@ -657,9 +708,9 @@ void hxo_lib_state(const hxo_group* g, struct hxo_libstate* L, const double* v) 
                 s[0] = s[0] + (1.0 - exp(dt * ((-1.0) / tau))) * (-(inf / tau) / ((-1.0) / tau) - s[0]);
                 continue;
             }
-            if (t == HXO_NCA_LR) continue; /* no STATE */
+            if (t == HXO_NCA_LR || t == HXO_CAINTERNM_LR) continue; /* no STATE of its own */
             if (is_worm(t)) { /* x + (1 - exp(dt ((-1) / tau))) (-(inf / tau) / ((-1) / tau) - x) */
-                double wr[6] = {0, 0, 0, 0, 0, 0};
+                double wr[8] = {0, 0, 0, 0, 0, 0, 0, 0};
                 worm_gates(t, v[i], p + 4, wr);
                 for (int q = 0; q < NST[t]; q++) {
                     const double inf = wr[2 * q], tau = wr[2 * q + 1];

@@ -10,7 +10,7 @@ int hxo_lib_alloc(const hxo_group* g, struct hxo_libstate** out);
 void hxo_lib_free(struct hxo_libstate* L);
 void hxo_lib_init(const hxo_group* g, struct hxo_libstate* L, const double* v);
 void hxo_lib_current(const hxo_group* g, struct hxo_libstate* L, const double* v, double* rhs, double* d);
-void hxo_lib_state_ion(const hxo_group* g, struct hxo_libstate* L);
+void hxo_lib_state_ion(const hxo_group* g, struct hxo_libstate* L, const double* v);
 void hxo_lib_state(const hxo_group* g, struct hxo_libstate* L, const double* v);
 int hxo_lib_final(const hxo_group* g, const struct hxo_libstate* L, double* out, int cap);
 

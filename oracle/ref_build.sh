@@ -35,7 +35,8 @@ SRCS=$(cd "$REF" && ls \
   mech/user-mech/Ca.cu mech/worm-lr-mech/shl1_lr.cu mech/worm-lr-mech/kvs1_lr.cu mech/worm-lr-mech/irk_lr.cu \
   mech/worm-lr-mech/egl36_lr.cu mech/worm-lr-mech/shk1_lr.cu mech/worm-lr-mech/egl2_lr.cu \
   mech/worm-lr-mech/cca1_lr.cu mech/worm-lr-mech/egl19_lr.cu mech/worm-lr-mech/unc2_lr.cu \
-  mech/worm-lr-mech/kcnl_lr.cu mech/worm-lr-mech/nca_lr.cu \
+  mech/worm-lr-mech/kcnl_lr.cu mech/worm-lr-mech/nca_lr.cu mech/worm-lr-mech/kqt3_lr.cu \
+  mech/worm-lr-mech/cainternm_lr.cu \
   2>/dev/null)
 
 compile() {

@@ -37,6 +37,8 @@ CASES = {
     "lib_cells": (lambda: synth.lib_tree_batch(2, seed0=700, nmax=200), 2000, None),
     # hh cells and library cells in one group
     "lib_mixed": (lambda: _lib_mixed(), 1200, None),
+    # library cells with the worm-lr calcium dynamics cainternm_lr
+    "lib_cainternm": (lambda: synth.lib_tree_batch(2, seed0=710, nmax=200, cadyn="cainternm_lr"), 2000, None),
 }
 
 

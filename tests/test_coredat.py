@@ -46,6 +46,7 @@ def _same(g, h):
         lambda: synth.spiking_network(),
         lambda: synth.coupled_network(),
         lambda: synth.lib_tree_batch(2, seed0=8, nmax=150),
+        lambda: synth.lib_tree_batch(2, seed0=9, nmax=150, cadyn="cainternm_lr"),
         lambda: _lib_mixed(),
     ],
 )

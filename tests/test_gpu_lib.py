@@ -34,8 +34,8 @@ def Sim():
     return S
 
 
-def _group():
-    return synth.lib_tree_batch(3, seed0=4100, nmax=160)
+def _group(cadyn="CaDynamics_E2"):
+    return synth.lib_tree_batch(3, seed0=4100, nmax=160, cadyn=cadyn)
 
 
 def _probes(g):
@@ -53,6 +53,17 @@ def test_forward_library_cells(Sim):
     assert err <= V_TOL, err
     up = (ref[1:, 0] > 0) & (ref[:-1, 0] <= 0)
     assert up.sum() >= 2  # the soma spikes: the channels are exercised
+
+
+def test_forward_library_cells_cainternm(Sim):
+    """The worm-lr calcium dynamics cainternm_lr in place of CaDynamics_E2."""
+    g = _group("cainternm_lr")
+    probes = _probes(g)
+    s = Sim(0)
+    s.load_group(g)
+    tr = s.simulate(2000, probes=probes)
+    ref, _ = O.forward(g, 2000, probe=probes)
+    assert np.max(np.abs(tr - ref)) / np.max(np.abs(ref)) <= V_TOL
 
 
 def test_forward_mixed_hh_and_library(Sim):
@@ -90,13 +101,19 @@ def test_library_gradients_vs_finite_differences(Sim):
     """Spiking (800 steps: the soma fires, calcium enters) and subthreshold
     (190 steps, before the IClamp: every voltage below -60 mV, so the K_Pst
     time constant stays on one branch of its v < -50 switch, K_Pst.cu rates)
-    regimes.  Every kind must agree in both; each kind must be resolved by
-    the finite differences to 1e-3 in one of them, and two thirds of them
-    to 1e-6 (the calcium-buffer parameters and the small densities move the
-    voltages least)."""
+    regimes with CaDynamics_E2, and the spiking regime with cainternm_lr as
+    the calcium dynamics (the kinds that read or write calcium, and
+    kqt3_lr).  Every kind must agree in every run; each kind must be
+    resolved by the finite differences to 1e-3 in one of them, and two
+    thirds of them to 1e-6 (the calcium-buffer parameters and the small
+    densities move the voltages least)."""
+    from heliox_b200.model import LIB_IONS
+
     best = {}
-    for T, h in ((800, 1e-3), (190, 1e-2)):
-        g = _group()
+    ca_keys = [k for k in LIB_KEYS if "ca" in LIB_IONS.get(k.split(".")[0], ()) or k.startswith("kqt3_lr.")]
+    for T, h, cadyn in ((800, 1e-3, "CaDynamics_E2"), (190, 1e-2, "CaDynamics_E2"), (800, 1e-3, "cainternm_lr")):
+        g = _group(cadyn)
+        keys = [k for k in (LIB_KEYS if cadyn == "CaDynamics_E2" else ca_keys) if k.split(".")[0] in g.lib]
         probes = _probes(g)
         rng = np.random.default_rng(17)
         c = rng.standard_normal((T + 1, probes.size)) * 1e-2
@@ -106,8 +123,8 @@ def test_library_gradients_vs_finite_differences(Sim):
         tr = s.forward_capture(T, probes=probes)
         ref, _ = O.forward(g, T, probe=probes)
         assert np.max(np.abs(tr - ref)) / np.max(np.abs(ref)) <= V_TOL
-        grads = s.backward(c, keys=LIB_KEYS)
-        for key in LIB_KEYS:
+        grads = s.backward(c, keys=keys)
+        for key in keys:
             mech, var = key.split(".")
             p = g.lib[mech].fields[var]
             u = rng.standard_normal(p.size)
@@ -118,6 +135,7 @@ def test_library_gradients_vs_finite_differences(Sim):
             assert abs(ad - fd) <= FD_TOL * abs(fd) + 4 * noise, (T, key, ad, fd, noise)
             best[key] = min(best.get(key, np.inf), noise / abs(fd))
         s.close()
+    assert set(best) == set(LIB_KEYS), set(LIB_KEYS) - set(best)
     assert all(r <= 1e-3 for r in best.values()), best
     assert sum(r <= FD_TOL for r in best.values()) >= (2 * len(LIB_KEYS)) // 3, best
 
@@ -148,6 +166,8 @@ def test_library_param_roundtrip_and_handles(Sim):
     s = Sim(0)
     s.load_group(g)
     for key in LIB_KEYS:
+        if key.split(".")[0] not in g.lib:
+            continue
         v = s.get_param_array(key)
         mech, var = key.split(".")
         assert np.array_equal(v, g.lib[mech].fields[var]), key

@@ -153,11 +153,12 @@ def test_network_adjoint_vs_fd_of_reference_forward():
 
 
 @needs_ref
-@pytest.mark.parametrize("seed", [1, 2])
-def test_oracle_library_cells_bit_exact_vs_reference_live(seed):
-    """The user-mech channel set, ions and calcium dynamics (library cells and
-    a teacher with perturbed channel densities) against the reference."""
-    g = synth.lib_tree_batch(2, seed0=3000 + seed, nmax=180)
+@pytest.mark.parametrize("seed,cadyn", [(1, "CaDynamics_E2"), (2, "CaDynamics_E2"), (3, "cainternm_lr")])
+def test_oracle_library_cells_bit_exact_vs_reference_live(seed, cadyn):
+    """The library channel set, ions and calcium dynamics (CaDynamics_E2 or
+    cainternm_lr; library cells and a teacher with perturbed channel
+    densities) against the reference."""
+    g = synth.lib_tree_batch(2, seed0=3000 + seed, nmax=180, cadyn=cadyn)
     teacher = synth.perturb_lib(g, 0.3, seed=seed)
     for grp in (g, teacher):
         probe = np.array(list(grp.soma_nodes()) + [grp.nnode - 1], dtype=np.int32)
