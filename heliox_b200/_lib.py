@@ -67,9 +67,15 @@ HX_P = {
     "nca_lr.w": 46,
     "kqt3_lr.w": 47,
     "cainternm_lr.vcell": 48,
+    "shl1.gbshl1": 49,
+    "kvs1.gbkvs1": 50,
+    "irk.gbirk": 51,
+    "egl36.gbegl36": 52,
+    "shk1.gbshk1": 53,
+    "egl2.gbegl2": 54,
 }
-HX_P_COUNT = 49
-HX_LIB_NTYPE = 33
+HX_P_COUNT = 55
+HX_LIB_NTYPE = 39
 
 
 class LibTable(C.Structure):

@@ -879,6 +879,17 @@ struct Kqt3Lr : WormBase {
     }
 };
 
+// worm-mech channels (src/mech/worm-mech/<name>.cu): the worm-lr sibling's
+// gates and current with p[0] = gb (trainable) and the fixed vector 1, -80
+// (their hard-coded reversal potential: gb ... (v + 80)), 0, then the
+// kinetics constants of their setparames (kvs1: its GLOBALs)
+struct Shl1 : Shl1Lr {};
+struct Kvs1 : Kvs1Lr {};
+struct Irk : IrkLr {};
+struct Egl36 : Egl36Lr {};
+struct Shk1 : Shk1Lr {};
+struct Egl2 : Egl2Lr {};
+
 // cainternm_lr.cu state_single_node: the calcium update c = cai_old + dt
 // alpha(c), alpha = -f ica 1e6 / (2 F vcell) - (c - caeq) / tca at or below
 // 60 mV (the drive term drops above), solved by the reference's Newton
@@ -937,7 +948,7 @@ __device__ __forceinline__ T cadyn(const T& cai, const T& ica, const T& gamma, c
 enum LibType : int {
     kNaIon = 0, kKIon, kCaIon, kCaDyn, kCaHVA, kCaLVAst, kIm, kKPst, kKTst, kNaTg, kNapEt2, kSKE2, kSKv31, kHdLa,
     kKmLa, kKcaLa, kIt2La, kKdrLa, kScaLa, kCaPlain, kShl1Lr, kKvs1Lr, kIrkLr, kEgl36Lr, kShk1Lr, kEgl2Lr, kCca1Lr,
-    kEgl19Lr, kUnc2Lr, kKcnlLr, kNcaLr, kKqt3Lr, kCainternmLr, kNType
+    kEgl19Lr, kUnc2Lr, kKcnlLr, kNcaLr, kKqt3Lr, kCainternmLr, kShl1, kKvs1, kIrk, kEgl36, kShk1, kEgl2, kNType
 };
 static_assert(kNType <= 64, "the per-node type mask (DevLib::mask) holds one bit per type");
 // first trainable kind of each type, relative to HX_P_CADYN_GAMMA (-1: none)
@@ -949,9 +960,9 @@ __host__ __device__ constexpr int nstate(int t) {
     return t == kCaIon ? 1
            : (t == kNcaLr || t == kCainternmLr) ? 0
            : t == kKqt3Lr ? 4
-           : (t == kShl1Lr || t == kEgl36Lr) ? 3
+           : (t == kShl1Lr || t == kEgl36Lr || t == kShl1 || t == kEgl36) ? 3
            : (t == kIm || t == kSKE2 || t == kSKv31 || t == kHdLa || t == kKmLa || t == kKcaLa || t == kKdrLa ||
-              t == kIrkLr || t == kEgl2Lr || t == kKcnlLr)
+              t == kIrkLr || t == kEgl2Lr || t == kKcnlLr || t == kIrk || t == kEgl2)
                ? 1
            : t >= kCaHVA ? 2
                          : 0;
@@ -961,7 +972,8 @@ __host__ __device__ constexpr int nfix(int t) {
            : t == kKmLa ? 5 : t == kKcaLa ? 4 : t == kIt2La ? 15 : t == kScaLa ? 4 : t == kShl1Lr ? 21
            : t == kKvs1Lr ? 15 : t == kIrkLr ? 11 : t == kEgl36Lr ? 8 : t == kShk1Lr ? 14 : t == kEgl2Lr ? 9
            : t == kCca1Lr ? 15 : t == kEgl19Lr ? 28 : t == kUnc2Lr ? 18 : t == kKcnlLr ? 5 : t == kNcaLr ? 2
-           : t == kKqt3Lr ? 28 : t == kCainternmLr ? 3 : 0;
+           : t == kKqt3Lr ? 28 : t == kCainternmLr ? 3 : t == kShl1 ? 21 : t == kKvs1 ? 15 : t == kIrk ? 11
+           : t == kEgl36 ? 8 : t == kShk1 ? 14 : t == kEgl2 ? 9 : 0;
 }
 __host__ __device__ constexpr int ntrain(int t) { return t < kCaDyn ? 0 : t == kCaDyn ? 4 : 1; }
 
@@ -993,7 +1005,13 @@ __host__ __device__ constexpr int ntrain(int t) { return t < kCaDyn ? 0 : t == k
     X(kUnc2Lr, Unc2Lr)     \
     X(kKcnlLr, KcnlLr)     \
     X(kNcaLr, NcaLr)       \
-    X(kKqt3Lr, Kqt3Lr)
+    X(kKqt3Lr, Kqt3Lr)     \
+    X(kShl1, Shl1)         \
+    X(kKvs1, Kvs1)         \
+    X(kIrk, Irk)           \
+    X(kEgl36, Egl36)       \
+    X(kShk1, Shk1)         \
+    X(kEgl2, Egl2)
 
 // ------------------------------------------------------------ drivers
 // one channel's forward contribution; returns I(v) (the ion current)

@@ -1,6 +1,6 @@
 // hx_runtime_lib.cu -- host side of the library mechanisms (hx_lib.cuh):
 // the per-node entry tables in GPU order, the parameter kinds
-// HX_P_CADYN_GAMMA .. HX_P_CAINTERNM_LR_VCELL, and the device arrays of DevLib.
+// HX_P_CADYN_GAMMA .. HX_P_EGL2_G, and the device arrays of DevLib.
 //
 // The reference keeps one instance table per mechanism type
 // (MechTemp::reg_node_indices / read_data_from_coredat,
@@ -33,11 +33,28 @@ const char* kTypeName[HX_LIB_NTYPE] = {"na_ion", "k_ion", "ca_ion",  "CaDynamics
                                        "kca_la", "it2_la", "kdr_la", "sca_la",        "Ca",
                                        "shl1_lr", "kvs1_lr", "irk_lr", "egl36_lr",    "shk1_lr",
                                        "egl2_lr", "cca1_lr", "egl19_lr", "unc2_lr", "kcnl_lr", "nca_lr",
-                                       "kqt3_lr", "cainternm_lr"};
+                                       "kqt3_lr", "cainternm_lr", "shl1", "kvs1", "irk", "egl36", "shk1",
+                                       "egl2"};
+
+// worm-mech channels (src/mech/worm-mech/<name>.cu): the device runs them
+// through their worm-lr sibling's gates with the fixed vector 1, -80 (the
+// hard-coded reversal potential), 0, then the kinetics constants of their
+// setparames (kvs1: its GLOBALs), in the worm-lr GLOBAL order
+const double kShl1K[18] = {11.2, 14.1, -33.1, 8.3, 13.8, -17.5, 12.9, -3.7, 6.5,
+                           1.9, 539.2, -28.2, 4.9, 27.3, 8422.0, -37.7, 6.4, 118.9};  // shl1.cu setparames
+const double kIrkK[8] = {-82.0, 13.0, 17.1, -17.8, 20.3, -43.4, 11.2, 3.8};            // irk.cu
+const double kEgl36K[5] = {63.0, 28.5, 355.0, 63.0, 13.0};                             // egl36.cu
+const double kShk1K[11] = {20.4, 7.7, -7.0, 5.8, 26.6, -33.7, 15.8, -33.7, 15.4, 2.0, 1400.0};  // shk1.cu
+const double kEgl2K[6] = {-6.9, 14.9, 1845.8, -122.6, 13.8, 1517.74};                  // egl2.cu
+bool worm_mech(int t) { return t >= HX_LIB_SHL1 && t <= HX_LIB_EGL2; }
 
 // columns of a type's hx_lib_table rows (trainable first, then fixed); hd_la's
 // GLOBALs q10 and qtl enter the device's fixed parameters as one factor
-int desc_cols(int t) { return t == HX_LIB_HD_LA ? 11 : hx::lib::ntrain(t) + hx::lib::nfix(t); }
+int desc_cols(int t) {
+    if (t == HX_LIB_HD_LA) return 11;
+    if (worm_mech(t)) return t == HX_LIB_KVS1 ? 13 : 1;
+    return hx::lib::ntrain(t) + hx::lib::nfix(t);
+}
 
 // ions a type needs on its node: bit 0 Na, 1 K, 2 Ca
 int ions_needed(int t) {
@@ -58,6 +75,12 @@ int ions_needed(int t) {
         case HX_LIB_SHK1_LR:
         case HX_LIB_EGL2_LR:
         case HX_LIB_KQT3_LR:
+        case HX_LIB_SHL1:
+        case HX_LIB_KVS1:
+        case HX_LIB_IRK:
+        case HX_LIB_EGL36:
+        case HX_LIB_SHK1:
+        case HX_LIB_EGL2:
             return 2;
         case HX_LIB_SK_E2:
         case HX_LIB_KCA_LA:
@@ -174,6 +197,11 @@ int hx_lib_load(hx_ctx* ctx, const hx_group_desc* desc) {
                 for (int c = 1; c <= 8; c++) fv.push_back(par[c]);
                 const double qt = std::pow(par[9], ((desc->celsius - 33.0) / 10.0));
                 fv.push_back(par[10] * qt * par[6]);
+            } else if (worm_mech(t)) {
+                fv = {1.0, -80.0, 0.0};
+                const double* k = t == HX_LIB_SHL1 ? kShl1K : t == HX_LIB_IRK ? kIrkK : t == HX_LIB_EGL36 ? kEgl36K
+                                  : t == HX_LIB_SHK1 ? kShk1K : t == HX_LIB_EGL2 ? kEgl2K : par + 1;
+                fv.insert(fv.end(), k, k + (nfx - 3));
             } else {
                 for (int c = 0; c < nfx; c++) fv.push_back(par[ntr + c]);
             }
@@ -199,12 +227,12 @@ int hx_lib_load(hx_ctx* ctx, const hx_group_desc* desc) {
     if (fix.empty()) fix.push_back(0.0);
     if (ent.empty()) ent.push_back(0);
     // GLOBALs of a mechanism: one value over its instances
-    const int glo_t[18] = {HX_LIB_SK_E2,    HX_LIB_HD_LA,    HX_LIB_KM_LA,   HX_LIB_KCA_LA,   HX_LIB_IT2_LA,
+    const int glo_t[19] = {HX_LIB_SK_E2,    HX_LIB_HD_LA,    HX_LIB_KM_LA,   HX_LIB_KCA_LA,   HX_LIB_IT2_LA,
                            HX_LIB_SCA_LA,   HX_LIB_SHL1_LR,  HX_LIB_KVS1_LR, HX_LIB_IRK_LR,   HX_LIB_EGL36_LR,
                            HX_LIB_SHK1_LR,  HX_LIB_EGL2_LR,  HX_LIB_CCA1_LR, HX_LIB_EGL19_LR, HX_LIB_UNC2_LR,
-                           HX_LIB_KCNL_LR,  HX_LIB_KQT3_LR,  HX_LIB_CAINTERNM_LR};
-    const int glo_c0[18] = {1, 3, 1, 1, 1, 3, 4, 4, 4, 4, 4, 4, 4, 4, 4, 3, 4, 1};
-    for (int u = 0; u < 18; u++) {
+                           HX_LIB_KCNL_LR,  HX_LIB_KQT3_LR,  HX_LIB_CAINTERNM_LR, HX_LIB_KVS1};
+    const int glo_c0[19] = {1, 3, 1, 1, 1, 3, 4, 4, 4, 4, 4, 4, 4, 4, 4, 3, 4, 1, 1};
+    for (int u = 0; u < 19; u++) {
         const hx_lib_table& T = D->t[glo_t[u]];
         const int nc = desc_cols(glo_t[u]);
         for (int j = 1; j < T.n; j++)

@@ -108,6 +108,14 @@ LIB_MECHS = (
     ("kqt3_lr", ("w", "gbkqt3", "ek_tmp", "dv") + KQT3_GLOBALS, 1),
     # cainternm_lr (calcium dynamics of the worm-lr set): vcell per instance, GLOBALs f, tca, caeq
     ("cainternm_lr", ("vcell", "f", "tca", "caeq"), 1),
+    # worm-mech channels (src/mech/worm-mech): gb ... (v + 80) with the kinetics hard-coded in setparames
+    # (kvs1: GLOBALs), gb trainable
+    ("shl1", ("gbshl1",), 1),
+    ("kvs1", ("gbkvs1",) + ("vhm", "ka", "vhh", "ki", "atm", "btm", "ctm", "dtm", "ath", "bth", "cth", "dth"), 1),
+    ("irk", ("gbirk",), 1),
+    ("egl36", ("gbegl36",), 1),
+    ("shk1", ("gbshk1",), 1),
+    ("egl2", ("gbegl2",), 1),
 )
 # fields that are GLOBALs of their mechanism in the reference (one value per
 # group, written to globals.dat as <field>_<mechanism>)
@@ -131,6 +139,7 @@ LIB_GLOBALS = {
     "kcnl_lr": ("kca", "a", "ek_tmp"),
     "kqt3_lr": KQT3_GLOBALS,
     "cainternm_lr": ("f", "tca", "caeq"),
+    "kvs1": ("vhm", "ka", "vhh", "ki", "atm", "btm", "ctm", "dtm", "ath", "bth", "cth", "dth"),
 }
 LIB_NAMES = tuple(m[0] for m in LIB_MECHS)
 LIB_FIELDS = {m[0]: m[1] for m in LIB_MECHS}
@@ -154,6 +163,7 @@ LIB_IONS = {
     "nca_lr": ("na",),
     "kqt3_lr": ("k",),
     "cainternm_lr": ("ca",),
+    "shl1": ("k",), "kvs1": ("k",), "irk": ("k",), "egl36": ("k",), "shk1": ("k",), "egl2": ("k",),
 }
 
 
@@ -443,6 +453,8 @@ LIB_STATES = {"ca_ion": ("cai",), "Ca_HVA": ("m", "h"), "Ca_LVAst": ("m", "h"), 
               "unc2_lr": ("m", "h"),
               "kcnl_lr": ("m",),
               "kqt3_lr": ("mf", "ms", "ww", "s"),
+              "shl1": ("m", "hf", "hs"), "kvs1": ("m", "h"), "irk": ("m",), "egl36": ("mf", "mm", "ms"),
+              "shk1": ("m", "h"), "egl2": ("m",),
 }
 
 

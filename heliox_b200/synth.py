@@ -261,6 +261,13 @@ LIB_DENSITY = {
     "kcnl_lr": (1e-4, 0.0, 1e-5),
     "nca_lr": (0.0, 0.0, 2e-6),
     "kqt3_lr": (2e-4, 0.0, 5e-5),
+    # worm-mech channels: gb per region
+    "shl1": (2e-4, 0.0, 0.0),
+    "kvs1": (0.0, 0.0, 2e-5),
+    "irk": (5e-5, 0.0, 5e-5),
+    "egl36": (0.0, 0.0, 5e-5),
+    "shk1": (1e-4, 1e-4, 0.0),
+    "egl2": (0.0, 0.0, 2e-5),
 }
 # GLOBALs of hd_la / km_la (one value per group; their published defaults,
 # km_la's tadj = 2.3^((34 - 23) / 10)) and hd_la's per-instance vhalfl, tau
@@ -284,6 +291,8 @@ LIB_LA_GLOBALS = {
     "cca1_lr": dict(vhm=-43.32, ka=7.6, vhh=-58.0, ki=7.0, atm=40.0, btm=-62.5, ctm=-12.6, dtm=0.7, ath=280.0, bth=-60.7, cth=8.5, dth=19.8),
     "egl19_lr": dict(vhm=5.6, ka=7.5, vhh=24.9, ki=12.0, vhhb=-20.5, kib=8.1, ahinf=1.43, bhinf=0.14, chinf=5.96, dhinf=0.6, atm=2.9, btm=5.2, ctm=6.0, dtm=1.9, etm=1.4, ftm=30.0, gtm=2.3, ath=0.4, bth=44.6, cth=-23.0, dth=5.0, eth=36.4, fth=28.7, gth=3.7, hth=43.1),
     "kcnl_lr": dict(kca=2e-4, a=50.0, ek_tmp=-80.0),
+    "kvs1": dict(vhm=57.1, ka=25.0, vhh=47.3, ki=11.1, atm=30.0, btm=18.1, ctm=20.0, dtm=1.0, ath=88.5, bth=50.0,
+                 cth=-15.0, dth=53.4),
     "kqt3_lr": dict(vhm=-12.8, ka=15.8, vhw=-1.1, kiw=28.8, aw=0.5, bw=0.5, vhs=-45.3, kis=12.3, bs=0.7,
                     atmf=395.3, btmf=38.1, ctmf=33.59, atms=5503.0, btms=-5345.4, ctms=0.02827, dtms=-23.9,
                     etms=-4590.6, ftms=0.0357, gtms=14.2, atw=0.5, btw=2.9, ctw=-48.09, dtw=48.83, ats=500.0,

@@ -20,7 +20,7 @@
 extern "C" {
 #endif
 
-#define HX_ABI_VERSION 4
+#define HX_ABI_VERSION 5
 
 typedef struct hx_ctx hx_ctx;
 
@@ -77,6 +77,11 @@ typedef struct hx_ctx hx_ctx;
  *   HX_LIB_CAINTERNM_LR (cainternm_lr.cu): vcell, then its GLOBALs f, tca,
  *                  caeq; calcium dynamics (writes cai in the state phase), at
  *                  most one of it and HX_LIB_CADYN per node
+ *   HX_LIB_SHL1, HX_LIB_IRK, HX_LIB_EGL36, HX_LIB_SHK1, HX_LIB_EGL2
+ *                  (src/mech/worm-mech/<name>.cu): gb (the kinetics are
+ *                  hard-coded in the mechanism, erev -80 mV); HX_LIB_KVS1: gb,
+ *                  then its GLOBALs vhm ka vhh ki atm btm ctm dtm ath bth cth
+ *                  dth; these need k_ion on their node
  * A channel needs its ion on its node (Na: NaTg, Nap_Et2; K: Im, K_Pst,
  * K_Tst, SK_E2, SKv3_1, km_la, kca_la, kdr_la; Ca: CaDynamics_E2, Ca_HVA,
  * Ca_LVAst, it2_la, sca_la, Ca, SK_E2 and kca_la (cai)); the worm-lr
@@ -118,7 +123,13 @@ enum hx_lib_type {
     HX_LIB_NCA_LR = 30,
     HX_LIB_KQT3_LR = 31,
     HX_LIB_CAINTERNM_LR = 32,
-    HX_LIB_NTYPE = 33
+    HX_LIB_SHL1 = 33,
+    HX_LIB_KVS1 = 34,
+    HX_LIB_IRK = 35,
+    HX_LIB_EGL36 = 36,
+    HX_LIB_SHK1 = 37,
+    HX_LIB_EGL2 = 38,
+    HX_LIB_NTYPE = 39
 };
 typedef struct hx_lib_table {
     int n;
@@ -239,7 +250,13 @@ enum hx_param_kind {
     HX_P_NCA_LR_W = 46,
     HX_P_KQT3_LR_W = 47,
     HX_P_CAINTERNM_LR_VCELL = 48, /* cainternm_lr: vcell per instance */
-    HX_P_COUNT = 49
+    HX_P_SHL1_G = 49,             /* worm-mech: gb per instance */
+    HX_P_KVS1_G = 50,
+    HX_P_IRK_G = 51,
+    HX_P_EGL36_G = 52,
+    HX_P_SHK1_G = 53,
+    HX_P_EGL2_G = 54,
+    HX_P_COUNT = 55
 };
 
 /* Statistics of the execution plan built at load time. */

@@ -30,6 +30,11 @@
  *                                        are not carried
  *   cainternm_lr                         src/mech/worm-lr-mech/cainternm_lr.cu (Newton
  *                                        solve of the implicit calcium update)
+ *   shl1, kvs1, irk, egl36, shk1, egl2   src/mech/worm-mech/<name>.cu: the worm-lr
+ *                                        gates with the kinetics hard-coded in
+ *                                        setparames (kvs1: GLOBALs), current
+ *                                        gb ... (v + 80), x + (1 - exp(-dt / tau))
+ *                                        (inf - x) (kvs1: exp(dt (-1 / tau)))
  * through MechTemp's finite-difference current (mech_template.cuh:589-648)
  * and the state phase order of nonvint_cpu (simulate.cpp:784-852: mechanisms
  * that write an ion in their state update first, then the others in type
@@ -46,9 +51,11 @@
 #define FD_EPS 0.001
 
 static const int NPAR[HXO_LIB_NTYPE] = {1, 1, 4, 4, 1, 1, 1, 1, 1, 5, 1, 2, 1, 11, 6, 5, 16, 1, 5, 1,
-                                        22, 16, 12, 9, 15, 10, 16, 29, 19, 6, 3, 29, 4};
+                                        22, 16, 12, 9, 15, 10, 16, 29, 19, 6, 3, 29, 4,
+                                        1, 13, 1, 1, 1, 1};
 static const int NST[HXO_LIB_NTYPE] = {0, 0, 0, 0, 2, 2, 1, 2, 2, 2, 2, 1, 1, 1, 1, 1, 2, 1, 2, 2,
-                                       3, 2, 1, 3, 2, 1, 2, 2, 2, 1, 0, 4, 0};
+                                       3, 2, 1, 3, 2, 1, 2, 2, 2, 1, 0, 4, 0,
+                                       3, 2, 1, 3, 2, 1};
 
 struct hxo_libstate {
     double* st[HXO_LIB_NTYPE]; /* n x NST per table */
@@ -351,6 +358,37 @@ static void worm_gates(int t, double v, const double* g, double r[8]) {
     }
 }
 
+/* worm-mech channels: the worm-lr type whose gates they share and their
+ * kinetics constants (setparames' locals, in the worm-lr GLOBAL order) */
+static int worm_lr_of(int t) {
+    switch (t) {
+        case HXO_SHL1: return HXO_SHL1_LR;
+        case HXO_KVS1: return HXO_KVS1_LR;
+        case HXO_IRK: return HXO_IRK_LR;
+        case HXO_EGL36: return HXO_EGL36_LR;
+        case HXO_SHK1: return HXO_SHK1_LR;
+        case HXO_EGL2: return HXO_EGL2_LR;
+    }
+    return -1;
+}
+static const double kShl1K[18] = {11.2, 14.1, -33.1, 8.3, 13.8, -17.5, 12.9, -3.7, 6.5,
+                                  1.9, 539.2, -28.2, 4.9, 27.3, 8422.0, -37.7, 6.4, 118.9};
+static const double kIrkK[8] = {-82.0, 13.0, 17.1, -17.8, 20.3, -43.4, 11.2, 3.8};
+static const double kEgl36K[5] = {63.0, 28.5, 355.0, 63.0, 13.0};
+static const double kShk1K[11] = {20.4, 7.7, -7.0, 5.8, 26.6, -33.7, 15.8, -33.7, 15.4, 2.0, 1400.0};
+static const double kEgl2K[6] = {-6.9, 14.9, 1845.8, -122.6, 13.8, 1517.74};
+static const double* worm_consts(int t, const double* p) {
+    switch (t) {
+        case HXO_SHL1: return kShl1K;
+        case HXO_KVS1: return p + 1; /* GLOBALs vhm_kvs1 .. dth_kvs1 */
+        case HXO_IRK: return kIrkK;
+        case HXO_EGL36: return kEgl36K;
+        case HXO_SHK1: return kShk1K;
+        case HXO_EGL2: return kEgl2K;
+    }
+    return NULL;
+}
+
 static int is_worm(int t) { return (t >= HXO_SHL1_LR && t <= HXO_NCA_LR) || t == HXO_KQT3_LR; }
 
 static double sk_zinf(double ca) {
@@ -447,6 +485,17 @@ static double chan_current(int t, double v, const double* p, const double* s, do
             const double ik_tmp = p[1] * (0.3 * s[0] + 0.7 * s[1]) * s[2] * s[3] * (v - erev);
             return p[0] * ik_tmp;
         }
+        /* worm-mech: gb ... (v + 80.0), erev = -80 (v - (-80) == v + 80 exactly) */
+        case HXO_SHL1:
+            return p[0] * s[0] * s[0] * s[0] * (0.7 * s[1] + 0.3 * s[2]) * (v - erev);
+        case HXO_KVS1:
+        case HXO_SHK1:
+            return p[0] * s[0] * s[1] * (v - erev);
+        case HXO_IRK:
+        case HXO_EGL2:
+            return p[0] * s[0] * (v - erev);
+        case HXO_EGL36:
+            return p[0] * (0.33 * s[0] + 0.36 * s[1] + 0.39 * s[2]) * (v - erev);
         default:
             return 0.0;
     }
@@ -455,9 +504,10 @@ static double chan_current(int t, double v, const double* p, const double* s, do
 /* 0: na, 1: k, 2: ca (the ion whose erev a channel reads and current it writes),
  * 3: none (hd_la: its own reversal potential ehd, no ion current), 4: its own
  * reversal potential ek_tmp (the worm-lr channels; their k current is not read;
- * kqt3_lr reads k_ion's ek) */
+ * kqt3_lr reads k_ion's ek), 5: -80 mV hard-coded (the worm-mech channels) */
 static int chan_ion(int t) {
     if (t == HXO_KQT3_LR) return 1;
+    if (worm_lr_of(t) >= 0) return 5;
     if (is_worm(t)) return 4;
     switch (t) {
         case HXO_HD_LA:
@@ -570,6 +620,12 @@ void hxo_lib_init(const hxo_group* g, struct hxo_libstate* L, const double* v) {
                 continue;
             }
             if (t == HXO_NCA_LR || t == HXO_CAINTERNM_LR) continue; /* no INITIAL of a state */
+            if (worm_lr_of(t) >= 0) { /* every gate at its steady state */
+                double wr[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+                worm_gates(worm_lr_of(t), v[i], worm_consts(t, p), wr);
+                for (int q = 0; q < NST[t]; q++) s[q] = wr[2 * q];
+                continue;
+            }
             if (is_worm(t)) { /* every gate at its steady state (kqt3_lr: mf = ms = 0) */
                 double wr[8] = {0, 0, 0, 0, 0, 0, 0, 0};
                 worm_gates(t, v[i], p + 4, wr);
@@ -600,7 +656,11 @@ void hxo_lib_current(const hxo_group* g, struct hxo_libstate* L, const double* v
             const int i = T->node[j];
             const double* p = T->par + NPAR[t] * j;
             const double* s = L->st[t] + NST[t] * j;
-            const double e = ion == 3 ? p[3] : t == HXO_KCNL_LR ? p[5] : ion == 4 ? p[2] : ion_erev(L, ion, i);
+            const double e = ion == 3   ? p[3]
+                             : ion == 5 ? -80.0
+                             : t == HXO_KCNL_LR ? p[5]
+                             : ion == 4 ? p[2]
+                                        : ion_erev(L, ion, i);
             double gg = chan_current(t, v[i] + 0.001, p, s, e);
             const double r = chan_current(t, v[i], p, s, e);
             if (ion == 2 || (t >= HXO_CCA1_LR && t <= HXO_UNC2_LR))
@@ -709,6 +769,18 @@ void hxo_lib_state(const hxo_group* g, struct hxo_libstate* L, const double* v) 
                 continue;
             }
             if (t == HXO_NCA_LR || t == HXO_CAINTERNM_LR) continue; /* no STATE of its own */
+            if (worm_lr_of(t) >= 0) {
+                double wr[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+                worm_gates(worm_lr_of(t), v[i], worm_consts(t, p), wr);
+                for (int q = 0; q < NST[t]; q++) {
+                    const double inf = wr[2 * q], tau = wr[2 * q + 1];
+                    if (t == HXO_KVS1)
+                        s[q] = s[q] + (1.0 - exp(dt * (-1.0 / tau))) * (inf - s[q]);
+                    else
+                        s[q] = s[q] + (1.0 - exp(-dt / tau)) * (inf - s[q]);
+                }
+                continue;
+            }
             if (is_worm(t)) { /* x + (1 - exp(dt ((-1) / tau))) (-(inf / tau) / ((-1) / tau) - x) */
                 double wr[8] = {0, 0, 0, 0, 0, 0, 0, 0};
                 worm_gates(t, v[i], p + 4, wr);
