@@ -73,9 +73,12 @@ HX_P = {
     "egl36.gbegl36": 52,
     "shk1.gbshk1": 53,
     "egl2.gbegl2": 54,
+    "cca1.gbcca1": 55,
+    "egl19.gbegl19": 56,
+    "unc2.gbunc2": 57,
 }
-HX_P_COUNT = 55
-HX_LIB_NTYPE = 39
+HX_P_COUNT = 58
+HX_LIB_NTYPE = 42
 
 
 class LibTable(C.Structure):

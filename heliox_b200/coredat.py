@@ -97,6 +97,9 @@ LIB_MECH_TABLE: List[Tuple[int, str, int, int, int, int, int, float]] = [
     (49, "egl36", 0, 0, 0, 12, 0, 0.0),
     (50, "shk1", 0, 0, 0, 9, 0, 0.0),
     (51, "egl2", 0, 0, 0, 6, 0, 0.0),
+    (52, "cca1", 0, 0, 0, 9, 0, 0.0),
+    (53, "egl19", 0, 0, 0, 9, 0, 0.0),
+    (54, "unc2", 0, 0, 0, 9, 0, 0.0),
 ]
 # data column of each library field (its var_in_coredata_idx); SK_E2.zTau is
 # the GLOBAL zTau_SK_E2 of globals.dat (SK_E2.cu:65-66)
@@ -123,7 +126,8 @@ LIB_COLUMNS = {
     "kqt3_lr": {"gbkqt3": 0, "ek_tmp": 1, "w": 2, "dv": 3},
     "cainternm_lr": {"vcell": 0},
     "shl1": {"gbshl1": 0}, "kvs1": {"gbkvs1": 0}, "irk": {"gbirk": 0}, "egl36": {"gbegl36": 0},
-    "shk1": {"gbshk1": 0}, "egl2": {"gbegl2": 0},
+    "shk1": {"gbshk1": 0}, "egl2": {"gbegl2": 0}, "cca1": {"gbcca1": 0}, "egl19": {"gbegl19": 0},
+    "unc2": {"gbunc2": 0},
 }
 # GLOBALs the loader requires of a mechanism that the dynamics do not read
 # (km_la.cu:70-80: its table parameters), written with these values

@@ -140,7 +140,7 @@ struct DevNet {
 // sca_la: inactF, actF, vshift, tadj; worm-lr: gb, ek_tmp, dv, kinetics).  Trainable
 // parameters (HX_P_CADYN_GAMMA .. HX_P_NCA_LR_W) live per instance in
 // prm[kind - HX_P_CADYN_GAMMA], their gradients in grad[...].
-constexpr int kLibKinds = 39;
+constexpr int kLibKinds = 42;
 struct DevLib {
     int nst;
     const int *node_off, *ent, *ent_st, *ent_fix;  // node_off: nnode + 1; ent_st: nent + 1

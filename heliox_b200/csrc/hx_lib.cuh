@@ -889,6 +889,9 @@ struct Irk : IrkLr {};
 struct Egl36 : Egl36Lr {};
 struct Shk1 : Shk1Lr {};
 struct Egl2 : Egl2Lr {};
+struct Cca1 : Cca1Lr {};  // calcium (current into ica): erev 60, gb ... (v - 60)
+struct Egl19 : Egl19Lr {};
+struct Unc2 : Unc2Lr {};
 
 // cainternm_lr.cu state_single_node: the calcium update c = cai_old + dt
 // alpha(c), alpha = -f ica 1e6 / (2 F vcell) - (c - caeq) / tca at or below
@@ -948,7 +951,8 @@ __device__ __forceinline__ T cadyn(const T& cai, const T& ica, const T& gamma, c
 enum LibType : int {
     kNaIon = 0, kKIon, kCaIon, kCaDyn, kCaHVA, kCaLVAst, kIm, kKPst, kKTst, kNaTg, kNapEt2, kSKE2, kSKv31, kHdLa,
     kKmLa, kKcaLa, kIt2La, kKdrLa, kScaLa, kCaPlain, kShl1Lr, kKvs1Lr, kIrkLr, kEgl36Lr, kShk1Lr, kEgl2Lr, kCca1Lr,
-    kEgl19Lr, kUnc2Lr, kKcnlLr, kNcaLr, kKqt3Lr, kCainternmLr, kShl1, kKvs1, kIrk, kEgl36, kShk1, kEgl2, kNType
+    kEgl19Lr, kUnc2Lr, kKcnlLr, kNcaLr, kKqt3Lr, kCainternmLr, kShl1, kKvs1, kIrk, kEgl36, kShk1, kEgl2, kCca1,
+    kEgl19, kUnc2, kNType
 };
 static_assert(kNType <= 64, "the per-node type mask (DevLib::mask) holds one bit per type");
 // first trainable kind of each type, relative to HX_P_CADYN_GAMMA (-1: none)
@@ -973,7 +977,8 @@ __host__ __device__ constexpr int nfix(int t) {
            : t == kKvs1Lr ? 15 : t == kIrkLr ? 11 : t == kEgl36Lr ? 8 : t == kShk1Lr ? 14 : t == kEgl2Lr ? 9
            : t == kCca1Lr ? 15 : t == kEgl19Lr ? 28 : t == kUnc2Lr ? 18 : t == kKcnlLr ? 5 : t == kNcaLr ? 2
            : t == kKqt3Lr ? 28 : t == kCainternmLr ? 3 : t == kShl1 ? 21 : t == kKvs1 ? 15 : t == kIrk ? 11
-           : t == kEgl36 ? 8 : t == kShk1 ? 14 : t == kEgl2 ? 9 : 0;
+           : t == kEgl36 ? 8 : t == kShk1 ? 14 : t == kEgl2 ? 9 : t == kCca1 ? 15 : t == kEgl19 ? 28
+           : t == kUnc2 ? 18 : 0;
 }
 __host__ __device__ constexpr int ntrain(int t) { return t < kCaDyn ? 0 : t == kCaDyn ? 4 : 1; }
 
@@ -1011,7 +1016,10 @@ __host__ __device__ constexpr int ntrain(int t) { return t < kCaDyn ? 0 : t == k
     X(kIrk, Irk)           \
     X(kEgl36, Egl36)       \
     X(kShk1, Shk1)         \
-    X(kEgl2, Egl2)
+    X(kEgl2, Egl2)         \
+    X(kCca1, Cca1)         \
+    X(kEgl19, Egl19)       \
+    X(kUnc2, Unc2)
 
 // ------------------------------------------------------------ drivers
 // one channel's forward contribution; returns I(v) (the ion current)

@@ -1,6 +1,6 @@
 // hx_runtime_lib.cu -- host side of the library mechanisms (hx_lib.cuh):
 // the per-node entry tables in GPU order, the parameter kinds
-// HX_P_CADYN_GAMMA .. HX_P_EGL2_G, and the device arrays of DevLib.
+// HX_P_CADYN_GAMMA .. HX_P_UNC2_G, and the device arrays of DevLib.
 //
 // The reference keeps one instance table per mechanism type
 // (MechTemp::reg_node_indices / read_data_from_coredat,
@@ -34,11 +34,11 @@ const char* kTypeName[HX_LIB_NTYPE] = {"na_ion", "k_ion", "ca_ion",  "CaDynamics
                                        "shl1_lr", "kvs1_lr", "irk_lr", "egl36_lr",    "shk1_lr",
                                        "egl2_lr", "cca1_lr", "egl19_lr", "unc2_lr", "kcnl_lr", "nca_lr",
                                        "kqt3_lr", "cainternm_lr", "shl1", "kvs1", "irk", "egl36", "shk1",
-                                       "egl2"};
+                                       "egl2", "cca1", "egl19", "unc2"};
 
 // worm-mech channels (src/mech/worm-mech/<name>.cu): the device runs them
 // through their worm-lr sibling's gates with the fixed vector 1, -80 (the
-// hard-coded reversal potential), 0, then the kinetics constants of their
+// hard-coded reversal potential; 60 for the calcium ones), 0, then the kinetics constants of their
 // setparames (kvs1: its GLOBALs), in the worm-lr GLOBAL order
 const double kShl1K[18] = {11.2, 14.1, -33.1, 8.3, 13.8, -17.5, 12.9, -3.7, 6.5,
                            1.9, 539.2, -28.2, 4.9, 27.3, 8422.0, -37.7, 6.4, 118.9};  // shl1.cu setparames
@@ -46,7 +46,13 @@ const double kIrkK[8] = {-82.0, 13.0, 17.1, -17.8, 20.3, -43.4, 11.2, 3.8};     
 const double kEgl36K[5] = {63.0, 28.5, 355.0, 63.0, 13.0};                             // egl36.cu
 const double kShk1K[11] = {20.4, 7.7, -7.0, 5.8, 26.6, -33.7, 15.8, -33.7, 15.4, 2.0, 1400.0};  // shk1.cu
 const double kEgl2K[6] = {-6.9, 14.9, 1845.8, -122.6, 13.8, 1517.74};                  // egl2.cu
-bool worm_mech(int t) { return t >= HX_LIB_SHL1 && t <= HX_LIB_EGL2; }
+const double kCca1K[12] = {-43.32, 7.6, -58.0, 7.0, 40.0, -62.5, -12.6, 0.7, 280.0, -60.7, 8.5, 19.8};  // cca1.cu
+const double kEgl19K[25] = {5.6, 7.5, 24.9, 12.0, -20.5, 8.1, 1.43, 0.14, 5.96, 0.60, 2.9, 5.2, 6.0,
+                            1.9, 1.4, 30.0, 2.3, 0.4, 44.6, -23.0, 5.0, 36.4, 28.7, 3.7, 43.1};  // egl19.cu
+const double kUnc2K[15] = {-12.2, 4.0, -52.5, 5.6, 1.5, -8.2, 9.1, 15.4, 0.1, 83.8, 52.9, -3.5, 72.1, 23.9, -3.6};  // unc2.cu
+bool worm_mech(int t) { return t >= HX_LIB_SHL1 && t <= HX_LIB_UNC2; }
+// the calcium ones: erev 60 mV (gb ... (v - 60)), current into ica
+bool worm_mech_ca(int t) { return t >= HX_LIB_CCA1 && t <= HX_LIB_UNC2; }
 
 // columns of a type's hx_lib_table rows (trainable first, then fixed); hd_la's
 // GLOBALs q10 and qtl enter the device's fixed parameters as one factor
@@ -94,6 +100,9 @@ int ions_needed(int t) {
         case HX_LIB_CCA1_LR:
         case HX_LIB_EGL19_LR:
         case HX_LIB_UNC2_LR:
+        case HX_LIB_CCA1:
+        case HX_LIB_EGL19:
+        case HX_LIB_UNC2:
             return 4;
         case HX_LIB_CADYN:
         case HX_LIB_CAINTERNM_LR:
@@ -198,9 +207,10 @@ int hx_lib_load(hx_ctx* ctx, const hx_group_desc* desc) {
                 const double qt = std::pow(par[9], ((desc->celsius - 33.0) / 10.0));
                 fv.push_back(par[10] * qt * par[6]);
             } else if (worm_mech(t)) {
-                fv = {1.0, -80.0, 0.0};
+                fv = {1.0, worm_mech_ca(t) ? 60.0 : -80.0, 0.0};
                 const double* k = t == HX_LIB_SHL1 ? kShl1K : t == HX_LIB_IRK ? kIrkK : t == HX_LIB_EGL36 ? kEgl36K
-                                  : t == HX_LIB_SHK1 ? kShk1K : t == HX_LIB_EGL2 ? kEgl2K : par + 1;
+                                  : t == HX_LIB_SHK1 ? kShk1K : t == HX_LIB_EGL2 ? kEgl2K : t == HX_LIB_CCA1 ? kCca1K
+                                  : t == HX_LIB_EGL19 ? kEgl19K : t == HX_LIB_UNC2 ? kUnc2K : par + 1;
                 fv.insert(fv.end(), k, k + (nfx - 3));
             } else {
                 for (int c = 0; c < nfx; c++) fv.push_back(par[ntr + c]);

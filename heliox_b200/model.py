@@ -116,6 +116,9 @@ LIB_MECHS = (
     ("egl36", ("gbegl36",), 1),
     ("shk1", ("gbshk1",), 1),
     ("egl2", ("gbegl2",), 1),
+    ("cca1", ("gbcca1",), 1),  # calcium: gb ... (v - 60), current into ica
+    ("egl19", ("gbegl19",), 1),
+    ("unc2", ("gbunc2",), 1),
 )
 # fields that are GLOBALs of their mechanism in the reference (one value per
 # group, written to globals.dat as <field>_<mechanism>)
@@ -164,6 +167,7 @@ LIB_IONS = {
     "kqt3_lr": ("k",),
     "cainternm_lr": ("ca",),
     "shl1": ("k",), "kvs1": ("k",), "irk": ("k",), "egl36": ("k",), "shk1": ("k",), "egl2": ("k",),
+    "cca1": ("ca",), "egl19": ("ca",), "unc2": ("ca",),
 }
 
 
@@ -454,7 +458,7 @@ LIB_STATES = {"ca_ion": ("cai",), "Ca_HVA": ("m", "h"), "Ca_LVAst": ("m", "h"), 
               "kcnl_lr": ("m",),
               "kqt3_lr": ("mf", "ms", "ww", "s"),
               "shl1": ("m", "hf", "hs"), "kvs1": ("m", "h"), "irk": ("m",), "egl36": ("mf", "mm", "ms"),
-              "shk1": ("m", "h"), "egl2": ("m",),
+              "shk1": ("m", "h"), "egl2": ("m",), "cca1": ("m", "h"), "egl19": ("m", "h"), "unc2": ("m", "h"),
 }
 
 

@@ -43,7 +43,7 @@ for _k in _lib.HX_P:
     if _m in ("CaDynamics_E2", "Ca_HVA", "Ca_LVAst", "Im", "K_Pst", "K_Tst", "NaTg", "Nap_Et2", "SK_E2", "SKv3_1",
               "hd_la", "km_la", "kca_la", "it2_la", "kdr_la", "sca_la", "Ca", "shl1_lr", "kvs1_lr", "irk_lr",
               "egl36_lr", "shk1_lr", "egl2_lr", "cca1_lr", "egl19_lr", "unc2_lr", "kcnl_lr", "nca_lr", "kqt3_lr",
-              "cainternm_lr", "shl1", "kvs1", "irk", "egl36", "shk1", "egl2"):
+              "cainternm_lr", "shl1", "kvs1", "irk", "egl36", "shk1", "egl2", "cca1", "egl19", "unc2"):
         _MECH_VAR[(_m, _v)] = _k
 _HANDLE_SHIFT = 24
 

@@ -268,6 +268,9 @@ LIB_DENSITY = {
     "egl36": (0.0, 0.0, 5e-5),
     "shk1": (1e-4, 1e-4, 0.0),
     "egl2": (0.0, 0.0, 2e-5),
+    "cca1": (0.0, 0.0, 5e-6),
+    "egl19": (0.0, 0.0, 5e-6),
+    "unc2": (0.0, 0.0, 5e-6),
 }
 # GLOBALs of hd_la / km_la (one value per group; their published defaults,
 # km_la's tadj = 2.3^((34 - 23) / 10)) and hd_la's per-instance vhalfl, tau

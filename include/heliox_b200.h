@@ -20,7 +20,7 @@
 extern "C" {
 #endif
 
-#define HX_ABI_VERSION 5
+#define HX_ABI_VERSION 6
 
 typedef struct hx_ctx hx_ctx;
 
@@ -82,6 +82,9 @@ typedef struct hx_ctx hx_ctx;
  *                  hard-coded in the mechanism, erev -80 mV); HX_LIB_KVS1: gb,
  *                  then its GLOBALs vhm ka vhh ki atm btm ctm dtm ath bth cth
  *                  dth; these need k_ion on their node
+ *   HX_LIB_CCA1, HX_LIB_EGL19, HX_LIB_UNC2 (src/mech/worm-mech/<name>.cu):
+ *                  gb (hard-coded kinetics, erev 60 mV, current into ica);
+ *                  they need ca_ion on their node
  * A channel needs its ion on its node (Na: NaTg, Nap_Et2; K: Im, K_Pst,
  * K_Tst, SK_E2, SKv3_1, km_la, kca_la, kdr_la; Ca: CaDynamics_E2, Ca_HVA,
  * Ca_LVAst, it2_la, sca_la, Ca, SK_E2 and kca_la (cai)); the worm-lr
@@ -129,7 +132,10 @@ enum hx_lib_type {
     HX_LIB_EGL36 = 36,
     HX_LIB_SHK1 = 37,
     HX_LIB_EGL2 = 38,
-    HX_LIB_NTYPE = 39
+    HX_LIB_CCA1 = 39,
+    HX_LIB_EGL19 = 40,
+    HX_LIB_UNC2 = 41,
+    HX_LIB_NTYPE = 42
 };
 typedef struct hx_lib_table {
     int n;
@@ -256,7 +262,10 @@ enum hx_param_kind {
     HX_P_EGL36_G = 52,
     HX_P_SHK1_G = 53,
     HX_P_EGL2_G = 54,
-    HX_P_COUNT = 55
+    HX_P_CCA1_G = 55,
+    HX_P_EGL19_G = 56,
+    HX_P_UNC2_G = 57,
+    HX_P_COUNT = 58
 };
 
 /* Statistics of the execution plan built at load time. */

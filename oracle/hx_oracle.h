@@ -80,7 +80,8 @@ enum {
     HXO_NATG, HXO_NAP_ET2, HXO_SK_E2, HXO_SKV3_1, HXO_HD_LA, HXO_KM_LA, HXO_KCA_LA, HXO_IT2_LA, HXO_KDR_LA,
     HXO_SCA_LA, HXO_CA, HXO_SHL1_LR, HXO_KVS1_LR, HXO_IRK_LR, HXO_EGL36_LR, HXO_SHK1_LR, HXO_EGL2_LR,
     HXO_CCA1_LR, HXO_EGL19_LR, HXO_UNC2_LR, HXO_KCNL_LR, HXO_NCA_LR,
-    HXO_KQT3_LR, HXO_CAINTERNM_LR, HXO_SHL1, HXO_KVS1, HXO_IRK, HXO_EGL36, HXO_SHK1, HXO_EGL2, HXO_LIB_NTYPE
+    HXO_KQT3_LR, HXO_CAINTERNM_LR, HXO_SHL1, HXO_KVS1, HXO_IRK, HXO_EGL36, HXO_SHK1, HXO_EGL2,
+    HXO_CCA1, HXO_EGL19, HXO_UNC2, HXO_LIB_NTYPE
 };
 typedef struct hxo_lib_table {
     int n;

@@ -30,7 +30,9 @@
  *                                        are not carried
  *   cainternm_lr                         src/mech/worm-lr-mech/cainternm_lr.cu (Newton
  *                                        solve of the implicit calcium update)
- *   shl1, kvs1, irk, egl36, shk1, egl2   src/mech/worm-mech/<name>.cu: the worm-lr
+ *   shl1, kvs1, irk, egl36, shk1, egl2,  src/mech/worm-mech/<name>.cu: the worm-lr
+ *   cca1, egl19, unc2 (calcium: i into
+ *   ica, erev 60 mV)
  *                                        gates with the kinetics hard-coded in
  *                                        setparames (kvs1: GLOBALs), current
  *                                        gb ... (v + 80), x + (1 - exp(-dt / tau))
@@ -52,10 +54,10 @@
 
 static const int NPAR[HXO_LIB_NTYPE] = {1, 1, 4, 4, 1, 1, 1, 1, 1, 5, 1, 2, 1, 11, 6, 5, 16, 1, 5, 1,
                                         22, 16, 12, 9, 15, 10, 16, 29, 19, 6, 3, 29, 4,
-                                        1, 13, 1, 1, 1, 1};
+                                        1, 13, 1, 1, 1, 1, 1, 1, 1};
 static const int NST[HXO_LIB_NTYPE] = {0, 0, 0, 0, 2, 2, 1, 2, 2, 2, 2, 1, 1, 1, 1, 1, 2, 1, 2, 2,
                                        3, 2, 1, 3, 2, 1, 2, 2, 2, 1, 0, 4, 0,
-                                       3, 2, 1, 3, 2, 1};
+                                       3, 2, 1, 3, 2, 1, 2, 2, 2};
 
 struct hxo_libstate {
     double* st[HXO_LIB_NTYPE]; /* n x NST per table */
@@ -368,15 +370,23 @@ static int worm_lr_of(int t) {
         case HXO_EGL36: return HXO_EGL36_LR;
         case HXO_SHK1: return HXO_SHK1_LR;
         case HXO_EGL2: return HXO_EGL2_LR;
+        case HXO_CCA1: return HXO_CCA1_LR;
+        case HXO_EGL19: return HXO_EGL19_LR;
+        case HXO_UNC2: return HXO_UNC2_LR;
     }
     return -1;
 }
+static int worm_mech_ca(int t) { return t == HXO_CCA1 || t == HXO_EGL19 || t == HXO_UNC2; }
 static const double kShl1K[18] = {11.2, 14.1, -33.1, 8.3, 13.8, -17.5, 12.9, -3.7, 6.5,
                                   1.9, 539.2, -28.2, 4.9, 27.3, 8422.0, -37.7, 6.4, 118.9};
 static const double kIrkK[8] = {-82.0, 13.0, 17.1, -17.8, 20.3, -43.4, 11.2, 3.8};
 static const double kEgl36K[5] = {63.0, 28.5, 355.0, 63.0, 13.0};
 static const double kShk1K[11] = {20.4, 7.7, -7.0, 5.8, 26.6, -33.7, 15.8, -33.7, 15.4, 2.0, 1400.0};
 static const double kEgl2K[6] = {-6.9, 14.9, 1845.8, -122.6, 13.8, 1517.74};
+static const double kCca1K[12] = {-43.32, 7.6, -58.0, 7.0, 40.0, -62.5, -12.6, 0.7, 280.0, -60.7, 8.5, 19.8};
+static const double kEgl19K[25] = {5.6, 7.5, 24.9, 12.0, -20.5, 8.1, 1.43, 0.14, 5.96, 0.60, 2.9, 5.2, 6.0,
+                                   1.9, 1.4, 30.0, 2.3, 0.4, 44.6, -23.0, 5.0, 36.4, 28.7, 3.7, 43.1};
+static const double kUnc2K[15] = {-12.2, 4.0, -52.5, 5.6, 1.5, -8.2, 9.1, 15.4, 0.1, 83.8, 52.9, -3.5, 72.1, 23.9, -3.6};
 static const double* worm_consts(int t, const double* p) {
     switch (t) {
         case HXO_SHL1: return kShl1K;
@@ -385,6 +395,9 @@ static const double* worm_consts(int t, const double* p) {
         case HXO_EGL36: return kEgl36K;
         case HXO_SHK1: return kShk1K;
         case HXO_EGL2: return kEgl2K;
+        case HXO_CCA1: return kCca1K;
+        case HXO_EGL19: return kEgl19K;
+        case HXO_UNC2: return kUnc2K;
     }
     return NULL;
 }
@@ -496,6 +509,11 @@ static double chan_current(int t, double v, const double* p, const double* s, do
             return p[0] * s[0] * (v - erev);
         case HXO_EGL36:
             return p[0] * (0.33 * s[0] + 0.36 * s[1] + 0.39 * s[2]) * (v - erev);
+        case HXO_CCA1: /* gb m m h (v - 60.0) */
+            return p[0] * s[0] * s[0] * s[1] * (v - erev);
+        case HXO_EGL19:
+        case HXO_UNC2:
+            return p[0] * s[0] * s[1] * (v - erev);
         default:
             return 0.0;
     }
@@ -504,7 +522,8 @@ static double chan_current(int t, double v, const double* p, const double* s, do
 /* 0: na, 1: k, 2: ca (the ion whose erev a channel reads and current it writes),
  * 3: none (hd_la: its own reversal potential ehd, no ion current), 4: its own
  * reversal potential ek_tmp (the worm-lr channels; their k current is not read;
- * kqt3_lr reads k_ion's ek), 5: -80 mV hard-coded (the worm-mech channels) */
+ * kqt3_lr reads k_ion's ek), 5: hard-coded (the worm-mech channels: -80 mV,
+ * the calcium ones 60 mV) */
 static int chan_ion(int t) {
     if (t == HXO_KQT3_LR) return 1;
     if (worm_lr_of(t) >= 0) return 5;
@@ -657,13 +676,13 @@ void hxo_lib_current(const hxo_group* g, struct hxo_libstate* L, const double* v
             const double* p = T->par + NPAR[t] * j;
             const double* s = L->st[t] + NST[t] * j;
             const double e = ion == 3   ? p[3]
-                             : ion == 5 ? -80.0
+                             : ion == 5 ? (worm_mech_ca(t) ? 60.0 : -80.0)
                              : t == HXO_KCNL_LR ? p[5]
                              : ion == 4 ? p[2]
                                         : ion_erev(L, ion, i);
             double gg = chan_current(t, v[i] + 0.001, p, s, e);
             const double r = chan_current(t, v[i], p, s, e);
-            if (ion == 2 || (t >= HXO_CCA1_LR && t <= HXO_UNC2_LR))
+            if (ion == 2 || (t >= HXO_CCA1_LR && t <= HXO_UNC2_LR) || worm_mech_ca(t))
                 L->ica[L->ca_of[i]] += r; /* worm-lr calcium: i into ica */
             gg = (gg - r) / FD_EPS;
             rhs[i] -= r;

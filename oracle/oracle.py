@@ -43,7 +43,7 @@ class _LibTable(C.Structure):
 
 
 class _Lib(C.Structure):
-    _fields_ = [("t", _LibTable * 39)]
+    _fields_ = [("t", _LibTable * 42)]
 
 
 class _Group(C.Structure):
