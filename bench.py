@@ -1,29 +1,26 @@
 #!/usr/bin/env python
-"""Benchmark of the hot path: forward + exact adjoint of a cell batch (config 2).
+"""Benchmark of the hot path: forward + exact adjoint, compartment-timesteps/s.
 
-One step = forward with tape (4000 fixed steps of dt 0.025 ms) over 1024
-seeded random-tree cells (hh + pas, somatic IClamp), the soma-voltage MSE
-against a teacher trace (conductances perturbed lognormally, sigma 0.2) and the
-reverse sweep producing every per-compartment conductance gradient.  The
-metric is forward+backward compartment-timesteps per second.
+Default line (config 4, the network configuration the metric is quoted on at
+1/2/4/8 GPUs): one event network of 10,000 seeded random-tree cells (hh +
+pas, somatic IClamp), 100 Exp2Syn per cell from random presynaptic cells plus
+one NetStim-driven Exp2Syn (5 Hz, noise 1), 8000 steps of dt 0.025 ms.  One
+step = forward with checkpointed tape, soma-voltage MSE against a teacher
+network (weights perturbed lognormally, sigma 0.2), and the reverse sweep
+producing every synaptic weight gradient.  On N GPUs the SAME network is
+sharded by cell (strong scaling); after every minimum-delay window the ranks
+all-gather their window spikes over NCCL.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--config 2|3|4|5|6]
 
-Multi-GPU runs are launched by torchrun, one process per GPU; every rank
-integrates its own 1024-cell batch (cells are independent: weak scaling, no
-data-path collective) and the time is the max over ranks.
-
-The other configurations of the same metric (not the headline line):
+Other configurations of the same metric (not the default line):
+  --config 2   1024 independent random-tree cells per GPU, 4000 steps (no
+               collective; weak scaling);
   --config 3   one 50,000-compartment cell (<= 40 branch levels), 2000 steps,
                split across CTAs (cooperative launch), gradients of every
                segment's conductances;
-  --config 4   event network: --ncell cells per GPU (default 10,000) of the
-               config-2 recipe, 100 Exp2Syn each plus one NetStim (5 Hz,
-               noise 1) per cell, 8000 steps; on N GPUs the network has
-               N x ncell cells, sharded by cell, spikes all-gathered over NCCL
-               once per minimum-delay window (weak scaling);
   --config 5   302 cells coupled by 900 HalfGap pairs and 2000 graded
-               synapses, 8000 steps (one step per launch);
+               synapses, 8000 steps (replicas on N GPUs);
   --config 6   library cells: --ncell random trees (default 1024, config-2
                morphology) carrying the user-mech channel set of a layer-5
                pyramidal cell with calcium dynamics (NaTg, Nap_Et2, K_Pst,
@@ -49,21 +46,20 @@ METRIC = "fwd+bwd compartment-timesteps/sec"
 UNIT = "comp-steps/s"
 T_STEPS = 4000
 NCELL = 1024
+NCELL_NET = 10000
 SEED0 = 20240
-# DRAM bytes per compartment-step of the backward kernel from the committed ncu
-# capture (profiles/fwd_bwd_kernels_config2_100steps.md: dram__bytes_read.sum +
-# dram__bytes_write.sum of the captured launch / its compartment-steps; the
-# capture runs the config-2 cells for 100 steps, and the per-step traffic does
-# not depend on the step count).
-BWD_DRAM_BYTES_PER_UNIT = 322.9
 
 
 def _alg_bytes(g):
-    """Algorithmic HBM bytes per timestep for the whole group, split forward/backward.
+    """Algorithmic HBM bytes per timestep for the whole group.
 
     Per compartment B_c = 8*(3 p_c + 8 s_c) + 12 (p_c parameters, s_c states):
     one forward, one checkpoint-recompute forward and one adjoint step.  The
-    forward kernel's share is 8*(p_c + 2 s_c) + 4, the backward's the rest.
+    forward's share is 8*(p_c + 2 s_c) + 4 (read parameters and states, write
+    the tape), the backward pass's the rest, of which the reverse kernel alone
+    (parameters, tape row, state adjoints read and written) moves
+    8*(p_c + 4 s_c) + 4.  Returns (forward, backward pass, reverse kernel,
+    total).
     """
     import numpy as np
 
@@ -79,12 +75,13 @@ def _alg_bytes(g):
     for nm, tab in g.lib.items():
         np.add.at(s, tab.nodes, len(LIB_STATES.get(nm, ())))
         np.add.at(p, tab.nodes, len(LIB_FIELDS[nm]))
-    fwd = 8 * (p + 2 * s) + 4
-    tot = 8 * (3 * p + 8 * s) + 12
     # event synapses: 2 states, 2 parameters each (188 B per instance-step)
     nsyn = g.expsyn.n + g.exp2syn.n
-    syn_fwd, syn_tot = nsyn * (8 * (2 + 2 * 2) + 4), nsyn * (8 * (3 * 2 + 8 * 2) + 12)
-    return (float(fwd.sum()) + syn_fwd, float((tot - fwd).sum()) + syn_tot - syn_fwd, float(tot.sum()) + syn_tot)
+    p_all, s_all, n_all = float(p.sum()) + 2 * nsyn, float(s.sum()) + 2 * nsyn, g.nnode + nsyn
+    fwd = 8 * (p_all + 2 * s_all) + 4 * n_all
+    tot = 8 * (3 * p_all + 8 * s_all) + 12 * n_all
+    rev = 8 * (p_all + 4 * s_all) + 4 * n_all
+    return fwd, tot - fwd, rev, tot
 
 
 def _peaks():
@@ -151,57 +148,66 @@ def _dist():
 
 
 # ----------------------------------------------------------------------------- CPU baseline
-def _cpu_cell_job(args):
-    """One cell on one host core: forward + adjoint, returns (units, seconds).
+def _cpu_sample(config: int):
+    """The bounded CPU sample of a configuration: (description, jobs, steps per
+    job).  A job is one independent unit the reference integrates in one
+    process (it is single-threaded and has no multi-process mode): a
+    config-2 cell, or a small network of the config-4 recipe (its own cells'
+    synapses and NetStims, sources among its 8 cells)."""
+    if config == 4:
+        return "8-cell networks of the config-4 recipe, 2000 steps each", "net8", 2000
+    return "cells of the config-2 batch, 4000 steps each", "cell", T_STEPS
+
+
+def _cpu_job(args):
+    """One job on one host core: forward + adjoint; returns (units, seconds).
 
     With the reference harness built (oracle/_ref), the forward is the
-    reference's own CPU integrator (its CoreNEURON loader, Simulate::fadvance);
-    the reverse sweep -- which the reference does not have -- is the oracle's,
-    timed as (oracle forward + adjoint) - (oracle forward).  Otherwise both
-    halves are the oracle port.
+    reference's own CPU integrator (its CoreNEURON loader, Simulate::
+    finitialize + fadvance), timed inside the harness around the integration
+    alone; the reverse sweep -- which the reference does not have -- is the
+    oracle's, timed inside the oracle around its reverse loop.  Otherwise the
+    forward is the oracle's taped forward, timed the same way.
     """
-    seed, nstep, use_ref = args
+    kind, seed, nstep, use_ref = args
     sys.path.insert(0, ROOT)
     import numpy as np
 
     from heliox_b200 import synth
     from oracle import oracle as O
 
-    g = synth.random_tree_cell(seed)
+    if kind == "net8":
+        g = synth.network_config4_shard(8, 0, 1, seed=1000 + seed)
+    else:
+        g = synth.random_tree_cell(seed)
     t0 = time.perf_counter()
     tr, _ = O.forward(g, nstep)
     t_fwd_port = time.perf_counter() - t0
     dLdv = np.zeros_like(tr)
     dLdv[1:] = 2.0 * tr[1:] / nstep
-    t0 = time.perf_counter()
-    O.adjoint(g, nstep, dLdv)
-    t_adj = time.perf_counter() - t0
-    t_bwd = max(t_adj - t_fwd_port, 0.0)
-    if use_ref:
-        t0 = time.perf_counter()
-        O.ref_forward(g, nstep)
-        t_fwd = time.perf_counter() - t0
-    else:
-        t_fwd = t_fwd_port
-    return g.nnode * nstep, t_fwd + t_bwd
+    _, gr = O.adjoint(g, nstep, dLdv)
+    t_rev = gr["reverse_s"]
+    t_fwd = O.ref_forward(g, nstep, timing=True)[2] if use_ref else t_fwd_port
+    return g.nnode * nstep, t_fwd + t_rev
 
 
-def cpu_baseline(ncell_sample: int, nstep: int, procs: int):
-    """Forward + adjoint of a cell sample on host cores; spawn pool (no CUDA in
-    the workers).  Returns (units per second over all cores, units, summed
-    per-core seconds / cores, kind)."""
+def cpu_baseline(config: int, njobs: int, procs: int):
+    """Forward + adjoint of a bounded sample on host cores (spawn pool, no CUDA
+    in the workers).  Returns (units per second over all cores, units, busy
+    seconds per core, kind, sample description)."""
     import multiprocessing as mp
 
     from oracle import oracle as O
 
     use_ref = O.ref_available()
+    desc, kind, nstep = _cpu_sample(config)
     ctx = mp.get_context("spawn")
-    jobs = [(SEED0 + c, nstep, use_ref) for c in range(ncell_sample)]
+    jobs = [(kind, SEED0 + c, nstep, use_ref) for c in range(njobs)]
     with ctx.Pool(procs) as pool:
-        res = pool.map(_cpu_cell_job, jobs)
+        res = pool.map(_cpu_job, jobs)
     units = sum(r[0] for r in res)
     busy = sum(r[1] for r in res) / procs  # all cores busy in parallel
-    return units / busy, units, busy, ("reference" if use_ref else "port")
+    return units / busy, units, busy, ("reference" if use_ref else "port"), f"{njobs} {desc}"
 
 
 # ----------------------------------------------------------------------------- reference arm
@@ -211,13 +217,14 @@ def run_reference(args):
         return 0
     procs = os.cpu_count() or 1
     vals = []
-    sample = 2 * max(procs, 8)
-    kind = "port"
+    njobs = max(procs, 8)
+    kind, desc = "port", ""
     for it in range(args.warmup + args.steps):
-        v, units, wall, kind = cpu_baseline(sample, T_STEPS, procs)
+        v, units, wall, kind, desc = cpu_baseline(args.config, njobs, procs)
         if it >= args.warmup:
             vals.append(v)
     value = statistics.median(vals)
+    fwd_by = "the reference's CPU integrator (timed inside its harness)" if kind == "reference" else "oracle port"
     line = {
         "impl": "reference",
         "metric": METRIC,
@@ -227,20 +234,25 @@ def run_reference(args):
         "steps": args.steps,
         "warmup": args.warmup,
         "higher_is_better": True,
-        "scaling": "weak",
+        "scaling": "strong" if args.config == 4 else "weak",
         "vs_baseline": None,
         "dtype": "f64",
         "data": "synthetic",
-        "config": {"workload": f"config2: {NCELL} random-tree cells x {T_STEPS} steps, fwd+bwd",
-                   "sample": f"{sample} cells x {T_STEPS} steps per step"},
+        "config": {"workload": _workload_name(args), "sample": f"{desc} per step, on {procs} host cores"},
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": procs, "kind": kind,
-                         "sample": f"{sample} cells of the config-2 batch, {T_STEPS} steps; forward: "
-                                   + ("the reference's CPU integrator" if kind == "reference" else "oracle port")
-                                   + ", adjoint: oracle port (the reference has none)"},
+                         "sample": f"{desc}; forward: {fwd_by}, adjoint: oracle port (the reference has none)"},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
     return 0
+
+
+def _workload_name(args) -> str:
+    return {2: f"config2: random-tree cells x {T_STEPS} steps per GPU, fwd+bwd",
+            3: "config3: one 50,000-compartment cell x 2000 steps, fwd+bwd",
+            4: f"config4: event network of {args.ncell or NCELL_NET} cells x 8000 steps, fwd+bwd",
+            5: "config5: 302 coupled cells x 8000 steps, fwd+bwd",
+            6: f"config6: library cells x {T_STEPS} steps per GPU, fwd+bwd"}[args.config]
 
 
 # ----------------------------------------------------------------------------- our arm
@@ -273,11 +285,18 @@ def run_ours(args):
     probes = W["probes"]
     ncomp = g.nnode
 
+    if W.get("exchange"):
+        # one window for all ranks: the smallest over the ranks' own bounds
+        wt = torch.tensor([W["window"]], dtype=torch.int64, device=dev)
+        dist.all_reduce(wt, op=dist.ReduceOp.MIN)
+        W["window"] = int(wt.item())
+        W["exchange_cap"] = W["cells_max"] * ((W["window"] + 1) // 2) + 1
+
     def new_sim(grp):
         sim = Sim(local)
         sim.set_stream(stream.cuda_stream)
         sim.load_group(grp, gid_base=W.get("gid_base", 0), nsrc_cells=W.get("nsrc_cells", 0))
-        if ws > 1 and W.get("exchange"):
+        if W.get("exchange"):
             from heliox_b200 import shard
 
             sim.set_window(W["window"])
@@ -287,7 +306,7 @@ def run_ours(args):
     tsim = new_sim(teacher)
     target_h = tsim.simulate(T, probes=probes)
     torch.cuda.synchronize()
-    if ws > 1 and W.get("exchange"):
+    if W.get("exchange"):
         tsim.set_exchange(None, 1)
     tsim.close()
     del tsim
@@ -354,6 +373,9 @@ def run_ours(args):
     _, nf = s.last_kernel_ms(0)
     _, nb = s.last_kernel_ms(1)
     gpu_launches = args.steps * (1 + nf + 2 + nb + len(keys))
+    # the reverse kernel alone (last timed step; a checkpointed backward
+    # alternates segment recompute and reverse launches)
+    rev_ms, nrev = s.last_kernel_ms(2)
 
     # ---- end to end through the public host-buffer API (params in, loss/grads out),
     # host buffers page-locked (inputs from pinned host memory, results read
@@ -367,14 +389,14 @@ def run_ours(args):
     tr_h = pinned_empty((T + 1, nprobe))
     dl_h = pinned_empty((T + 1, nprobe))
     grads_h = {k: pinned_empty(counts[k]) for k in keys}
-    if not (ws > 1 and W.get("exchange")):  # the exchange hook runs on torch's stream
+    if not W.get("exchange"):  # host API on the context's own stream
         s.set_stream(0)
     torch.cuda.synchronize()
     h2d = sum(v.nbytes for v in host_params.values()) + (T + 1) * nprobe * 8
     d2h = (T + 1) * nprobe * 8 + sum(8 * counts[k] for k in keys)
     if dist:
         dist.barrier()
-    e2e_steps = args.steps if args.config == 2 else 1
+    e2e_steps = args.steps if args.config == 2 else min(args.steps, 2)
     t0 = time.perf_counter()
     for _ in range(e2e_steps):
         for k in keys:
@@ -389,14 +411,17 @@ def run_ours(args):
         dist.barrier()
 
     # ---- max over ranks
-    vals = torch.tensor([ms, e2e_s, fwd_ms, bwd_ms, float(ncomp)], dtype=torch.float64, device=dev)
+    fb, bb, rb, tb = _alg_bytes(g)
+    vals = torch.tensor([ms, e2e_s, fwd_ms, bwd_ms, rev_ms, float(ncomp), fb, bb, rb, tb], dtype=torch.float64,
+                        device=dev)
     if dist:
         mx = vals.clone()
         dist.all_reduce(mx, op=dist.ReduceOp.MAX)
         tot = vals.clone()
         dist.all_reduce(tot, op=dist.ReduceOp.SUM)
-        ms, e2e_s, fwd_ms, bwd_ms = (float(x) for x in mx[:4])
-        total_comp = float(tot[4])
+        ms, e2e_s, fwd_ms, bwd_ms, rev_ms = (float(x) for x in mx[:5])
+        total_comp = float(tot[5])
+        fb, bb, rb, tb = (float(x) for x in mx[6:10])  # the slowest rank's share bounds the kernel times
     else:
         total_comp = float(ncomp)
     units_per_step = total_comp * T
@@ -405,8 +430,9 @@ def run_ours(args):
 
     if rank == 0:
         peak, peak_src = _peaks()
-        fb, bb, tb = _alg_bytes(g)
-        achieved = bb * T / (bwd_ms / 1e3) / 1e9  # GB/s, backward kernel (dominant)
+        # roofline of the reverse kernel (the dominant one): its algorithmic bytes
+        # per launch / its mean launch time (CUDA events on the launch stream)
+        achieved = rb * T / (rev_ms / 1e3) / 1e9
         line = {
             "metric": METRIC,
             "value": value,
@@ -416,12 +442,13 @@ def run_ours(args):
             "warmup": args.warmup,
             "ms_per_step": ms / args.steps,
             "higher_is_better": True,
-            "scaling": "weak",
+            "scaling": W["scaling"],
             "vs_baseline": None,
             "dtype": "f64",
             "data": "synthetic",
             "config": {
                 "workload": W["workload"],
+                "compartments_total": int(total_comp),
                 "compartments_per_gpu": ncomp,
                 "parallelism": W["parallelism"].format(ws=ws),
                 "l2": "tape exceeds L2; 256 MiB flush write between steps",
@@ -433,30 +460,31 @@ def run_ours(args):
             "bwd_ms": bwd_ms,
             "roofline": {
                 "bound": "hbm",
-                "kernel": "bwd_kernel",
+                "kernel": "bwd_kernel" + ("<net>" if g.has_network else ""),
                 "achieved": achieved,
                 "peak": peak,
                 "peak_source": peak_src,
                 "unit": "GB/s",
                 "frac": achieved / peak,
-                "traffic": (BWD_DRAM_BYTES_PER_UNIT * units_per_step / ws
-                            if BWD_DRAM_BYTES_PER_UNIT and args.config == 2 else None),
-                "alg_bytes_per_launch": bb * T,
+                "traffic": None,
+                "alg_bytes_per_launch": rb * T / max(nrev, 1),
+                "launches_per_step": nrev,
+                "kernel_ms_per_step": rev_ms,
                 "fwd_frac": (fb * T / (fwd_ms / 1e3) / 1e9) / peak,
+                "bwd_pass_frac": (bb * T / (bwd_ms / 1e3) / 1e9) / peak,
                 "path_frac": (tb * T / ((fwd_ms + bwd_ms) / 1e3) / 1e9) / peak,
             },
             "clocks": clocks,
         }
-        if ws == 1 and not args.no_cpu and args.config == 2:
+        if ws == 1 and not args.no_cpu and args.config in (2, 4):
             procs = os.cpu_count() or 1
-            ns = 4 * max(procs, 8)
-            v, units, wall, kind = cpu_baseline(ns, T, procs)
+            v, units, wall, kind, desc = cpu_baseline(args.config, 2 * max(procs, 8), procs)
             fwd_by = "the reference's CPU integrator" if kind == "reference" else "oracle port"
             line["cpu_baseline"] = {"value": v, "unit": UNIT, "cores": procs, "kind": kind,
-                                    "sample": f"{ns} cells of the config-2 batch, {T} steps; forward: {fwd_by}, "
-                                              f"adjoint: oracle port; {wall:.1f} s per core"}
+                                    "sample": f"{desc}; forward: {fwd_by}, adjoint: oracle port; "
+                                              f"{wall:.1f} s per core"}
         print(json.dumps(line), flush=True)
-    if ws > 1 and W.get("exchange"):
+    if W.get("exchange"):
         s.set_exchange(None, 1)
     s.close()
     if dist:
@@ -471,11 +499,12 @@ def build_workload(args, ws, rank):
     from heliox_b200 import shard, synth
 
     if args.config == 2:
+        ncell = args.ncell or NCELL
         seed0 = SEED0 + 100000 * rank
-        g = synth.random_tree_batch(args.ncell, seed0=seed0)
+        g = synth.random_tree_batch(ncell, seed0=seed0)
         return {"group": g, "teacher": synth.perturb_conductances(g, 0.2, seed=seed0 + 7), "nstep": args.nstep,
-                "keys": ("hh.gnabar", "hh.gkbar", "hh.gl", "pas.g"), "probes": g.soma_nodes(),
-                "workload": f"config2: {args.ncell} seeded random-tree cells per GPU (hh+pas, IClamp), "
+                "keys": ("hh.gnabar", "hh.gkbar", "hh.gl", "pas.g"), "probes": g.soma_nodes(), "scaling": "weak",
+                "workload": f"config2: {ncell} seeded random-tree cells per GPU (hh+pas, IClamp), "
                             f"{args.nstep} steps dt 0.025 ms, soma-MSE vs lognormal teacher, forward + exact adjoint",
                 "parallelism": "cells sharded, {ws} GPU(s), no collective on the data path"}
     if args.config == 3:
@@ -483,26 +512,25 @@ def build_workload(args, ws, rank):
         probes = np.unique(np.linspace(0, g.nnode - 1, 64).astype(np.int32))
         T = 2000 if args.nstep == T_STEPS else args.nstep
         return {"group": g, "teacher": synth.perturb_conductances(g, 0.2, seed=SEED0 + 3), "nstep": T,
-                "keys": ("hh.gnabar", "hh.gkbar", "hh.gl", "pas.g"), "probes": probes,
+                "keys": ("hh.gnabar", "hh.gkbar", "hh.gl", "pas.g"), "probes": probes, "scaling": "weak",
                 "workload": f"config3: one {g.nnode}-compartment random tree ({g.meta.get('levels')} branch levels), "
                             f"{T} steps, MSE at 64 probes vs lognormal teacher, gradients of every segment's "
                             "conductances; split across CTAs (cooperative launch)",
                 "parallelism": "replicas: one cell per GPU ({ws} GPU(s))"}
     if args.config == 4:
-        ncell = args.ncell if args.ncell != NCELL else 10000
+        total = args.ncell or NCELL_NET
         T = 8000 if args.nstep == T_STEPS else args.nstep
-        g = synth.network_config4_shard(ncell, rank, ws)
+        g = synth.network_config4_shard(total, rank, ws)
         teacher = g.copy()
-        rng = np.random.default_rng(SEED0 + 4)
-        teacher.exp2syn.fields["weight"] = teacher.exp2syn.fields["weight"] * np.exp(
-            0.2 * rng.standard_normal(teacher.exp2syn.n))
-        W = shard.window_of(g)
+        teacher.exp2syn.fields["weight"] = g.meta["teacher_weight"].copy()
+        c0, c1 = synth.config4_cell_range(total, rank, ws)
         return {"group": g, "teacher": teacher, "nstep": T, "keys": ("Exp2Syn.weight", "hh.gnabar"),
-                "probes": g.soma_nodes(), "gid_base": rank * ncell, "nsrc_cells": ws * ncell, "exchange": ws > 1,
-                "window": W, "exchange_cap": ncell * ((W + 1) // 2) + 1,
-                "workload": f"config4: event network, {ncell} cells per GPU x 100 Exp2Syn + 1 NetStim (5 Hz) "
-                            f"each, {T} steps, soma MSE vs teacher (weights perturbed), weight gradients",
-                "parallelism": "cells sharded over {ws} GPU(s); window spike all-gather over NCCL"}
+                "probes": g.soma_nodes(), "gid_base": c0, "nsrc_cells": total, "exchange": ws > 1,
+                "window": shard.window_of(g), "cells_max": -(-total // ws), "scaling": "strong",
+                "workload": f"config4: event network of {total} cells (hh+pas random trees, IClamp) x 100 Exp2Syn "
+                            f"from random cells + 1 NetStim (5 Hz, noise 1) each, {T} steps dt 0.025 ms, soma MSE vs "
+                            "teacher (weights perturbed lognormally), weight and gnabar gradients",
+                "parallelism": "one network sharded by cell over {ws} GPU(s); window spike all-gather over NCCL"}
     if args.config == 5:
         g = synth.worm_config5()
         teacher = g.copy()
@@ -510,19 +538,20 @@ def build_workload(args, ws, rank):
         teacher.halfgap.fields["g"] = teacher.halfgap.fields["g"] * np.exp(0.2 * rng.standard_normal(g.halfgap.n))
         teacher.graded.fields["w"] = teacher.graded.fields["w"] * np.exp(0.2 * rng.standard_normal(g.graded.n))
         T = 8000 if args.nstep == T_STEPS else args.nstep
-        return {"group": g, "teacher": teacher, "nstep": T,
+        return {"group": g, "teacher": teacher, "nstep": T, "scaling": "weak",
                 "keys": ("HalfGap.g", "neuron_to_neuron_syn_lr.w", "hh.gnabar"), "probes": g.soma_nodes(),
                 "workload": f"config5: {g.ncell} cells, {g.halfgap.n // 2} HalfGap pairs, {g.graded.n} graded "
                             f"synapses, {T} steps, soma MSE vs teacher, gap and synapse gradients",
                 "parallelism": "replicas only ({ws} GPU(s)): coupled every step"}
     if args.config == 6:
+        ncell = args.ncell or NCELL
         seed0 = 51000 + 100000 * rank
-        g = synth.lib_tree_batch(args.ncell, seed0=seed0, nmin=200, nmax=1000, channels=synth.LIB_BBP_CHANNELS)
+        g = synth.lib_tree_batch(ncell, seed0=seed0, nmin=200, nmax=1000, channels=synth.LIB_BBP_CHANNELS)
         keys = ("NaTg.gNaTgbar", "Nap_Et2.gNap_Et2bar", "K_Pst.gK_Pstbar", "K_Tst.gK_Tstbar", "SKv3_1.gSKv3_1bar",
                 "SK_E2.gSK_E2bar", "Im.gImbar", "Ca_HVA.gbar", "Ca_LVAst.gCa_LVAstbar", "CaDynamics_E2.gamma")
         return {"group": g, "teacher": synth.perturb_lib(g, 0.2, seed=seed0 + 7), "nstep": args.nstep, "keys": keys,
-                "probes": g.soma_nodes(),
-                "workload": f"config6: {args.ncell} seeded random-tree library cells per GPU (user-mech channel set "
+                "probes": g.soma_nodes(), "scaling": "weak",
+                "workload": f"config6: {ncell} seeded random-tree library cells per GPU (user-mech channel set "
                             f"+ CaDynamics_E2 + pas, IClamp), {args.nstep} steps dt 0.025 ms, soma-MSE vs lognormal "
                             "teacher, forward + exact adjoint",
                 "parallelism": "cells sharded, {ws} GPU(s), no collective on the data path"}
@@ -535,10 +564,10 @@ def main():
     ap.add_argument("--steps", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=("ours", "reference"))
-    ap.add_argument("--ncell", type=int, default=NCELL)
+    ap.add_argument("--ncell", type=int, default=0, help="cells (config 4: of the whole network; 2/6: per GPU)")
     ap.add_argument("--nstep", type=int, default=T_STEPS)
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU-baseline leg")
-    ap.add_argument("--config", type=int, default=2, choices=(2, 3, 4, 5, 6))
+    ap.add_argument("--config", type=int, default=4, choices=(2, 3, 4, 5, 6))
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

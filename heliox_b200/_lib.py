@@ -135,6 +135,8 @@ class GroupDesc(C.Structure):
 
 # int (*)(void* user, const void* send_dev, void* recv_dev, int cap_entries, void* stream)
 EXCHANGE_FN = C.CFUNCTYPE(C.c_int, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_void_p)
+# int (*)(void* user, double* grad_dev, int n, void* stream)
+ALLREDUCE_FN = C.CFUNCTYPE(C.c_int, C.c_void_p, C.c_void_p, C.c_int, C.c_void_p)
 
 
 class PlanStats(C.Structure):
@@ -191,6 +193,7 @@ SIGNATURES = {
     "hx_opt_grads_from_backward": (C.c_int, [C.c_void_p, C.c_int, C.c_double]),
     "hx_opt_grad_buffer": (C.c_int, [C.c_void_p, C.c_int, C.POINTER(C.c_void_p), _ip]),
     "hx_opt_step": (C.c_int, [C.c_void_p, C.c_int, C.c_double, C.c_double]),
+    "hx_opt_set_allreduce": (C.c_int, [C.c_void_p, C.c_int, ALLREDUCE_FN, C.c_void_p]),
     "hx_opt_get_adam_state": (C.c_int, [C.c_void_p, C.c_int, C.POINTER(C.c_longlong), _dp, _dp, C.c_int, _dp]),
     "hx_opt_set_adam_state": (C.c_int, [C.c_void_p, C.c_int, C.c_longlong, _dp, _dp, C.c_int, _dp]),
     "hx_opt_reset": (C.c_int, [C.c_void_p, C.c_int]),
@@ -199,6 +202,7 @@ SIGNATURES = {
     "hx_set_exchange": (C.c_int, [C.c_void_p, EXCHANGE_FN, C.c_void_p, C.c_int, C.c_int]),
     "hx_set_window": (C.c_int, [C.c_void_p, C.c_int]),
     "hx_get_window": (C.c_int, [C.c_void_p, _ip]),
+    "hx_exchange_merge_status": (C.c_int, [_ip, C.c_int, _ip, _ip, _ip]),
 }
 
 _LIB = None

@@ -71,6 +71,8 @@ struct AdamOpt {
     DevBuf<int> kind, slot, flat;
     DevBuf<double> grad, m, v;
     DevBuf<float> f32;
+    hx_allreduce_fn allreduce = nullptr;  // sum of the slot gradients over ranks before each step
+    void* allreduce_user = nullptr;
 };
 
 struct hx_ctx {
@@ -121,6 +123,10 @@ struct hx_ctx {
     DevBuf<double*> prm_ptrs;  // device copy of prm[kind].p
     cudaEvent_t ev[4] = {nullptr, nullptr, nullptr, nullptr};
     int launches[2] = {0, 0};
+    // event pairs around every reverse-kernel launch of the last backward
+    // (a checkpointed backward alternates recompute and reverse launches)
+    std::vector<cudaEvent_t> kev;
+    int kev_n = 0;
 
     // ---- network (hx_runtime_net.cu)
     bool net = false, coupled = false;
@@ -142,6 +148,7 @@ struct hx_ctx {
     DevBuf<int> ev_cnt, ev_syn, dev_err;
     int ev_cap = 0;
     DevBuf<int2> win_send, win_recv, spk_log, ns_spk;
+    DevBuf<int2> st_send, st_recv;  // per-rank status pair after the last window
     DevBuf<int> win_n, log_n;
     int win_cap = 0, log_cap = 0, win_cap_user = 0;
     // NetStim trains of the last forward length (host generator, routed each forward)
@@ -176,6 +183,8 @@ int hx_fail(hx_ctx* c, const std::string& m);
 int hx_setup_probes(hx_ctx* ctx, int nprobe, const int* probe_nodes);
 hx::DevProbe hx_probe_view(hx_ctx* c);
 int hx_setup_time(hx_ctx* ctx, int nstep);
+// records the next event of the reverse-kernel pairs on stream st (kev_n = 0 starts a backward)
+int hx_kev_mark(hx_ctx* ctx, cudaStream_t st);
 double* hx_kind_ptr(hx_ctx* c, int kind);
 size_t hx_grad_base(const hx_ctx* c, int kind);
 // library mechanisms (hx_runtime_lib.cu): entry tables, kinds 16.. maps and

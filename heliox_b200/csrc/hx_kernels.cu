@@ -824,6 +824,27 @@ __global__ void log_advance_kernel(const int* __restrict__ win_n, int win_cap, i
     *log_n += min(*win_n, win_cap);
 }
 
+// A rank's status after its last window: (error bits | extra, largest bucket
+// count over the nstep steps).  One block; the ranks all-gather it.
+__global__ void net_status_kernel(const int* __restrict__ err, const int* __restrict__ ev_cnt, int nstep, int extra,
+                                  int2* out) {
+    __shared__ int red[256];
+    int m = 0;
+    for (int k = threadIdx.x; k < nstep; k += blockDim.x) m = max(m, ev_cnt[k]);
+    red[threadIdx.x] = m;
+    __syncthreads();
+    for (int s = blockDim.x / 2; s > 0; s >>= 1) {
+        if ((int)threadIdx.x < s) red[threadIdx.x] = max(red[threadIdx.x], red[threadIdx.x + s]);
+        __syncthreads();
+    }
+    if (threadIdx.x == 0) *out = make_int2(*err | extra, red[0]);
+}
+
+cudaError_t launch_net_status(const int* err, const int* ev_cnt, int nstep, int extra, int2* out, cudaStream_t st) {
+    net_status_kernel<<<1, 256, 0, st>>>(err, ev_cnt, nstep, extra, out);
+    return cudaGetLastError();
+}
+
 cudaError_t launch_syn_prep(int n, const int* kind, const double* tau1, const double* tau2, double dt, double* cA,
                             double* cB, double* fA, double* fB, cudaStream_t st) {
     if (n <= 0) return cudaSuccess;

@@ -159,6 +159,8 @@ int hx_destroy(hx_ctx* ctx) {
     cudaStreamSynchronize(ctx->st);
     for (auto& e : ctx->ev)
         if (e) cudaEventDestroy(e);
+    for (cudaEvent_t e : ctx->kev)
+        if (e) cudaEventDestroy(e);
     if (ctx->own) cudaStreamDestroy(ctx->own);
     for (AdamOpt* o : ctx->opts) delete o;
     delete ctx;
@@ -713,6 +715,17 @@ static int copy_ck(hx_ctx* ctx, int s, bool save) {
     return 0;
 }
 
+int hx_kev_mark(hx_ctx* ctx, cudaStream_t st) {
+    if (ctx->kev_n >= (int)ctx->kev.size()) {
+        cudaEvent_t e = nullptr;
+        HXC(cudaEventCreate(&e));
+        ctx->kev.push_back(e);
+    }
+    HXC(cudaEventRecord(ctx->kev[ctx->kev_n], st));
+    ctx->kev_n++;
+    return 0;
+}
+
 // plain or split-cell kernels (the split ones reset their barrier state per launch)
 static cudaError_t fwd_launch(hx_ctx* ctx, const hx::DevState& S, const hx::DevTape& T, int write_tape,
                               const hx::DevProbe& PV, double* trace, int k0, int k1) {
@@ -810,10 +823,13 @@ static int run_backward(hx_ctx* ctx, const double* dLdv_dev) {
     hx::DevState S = state_view(ctx);
     if (ctx->split) HXC(cudaMemsetAsync(ctx->split_err.p, 0, 4, ctx->st));
     HXC(cudaEventRecord(ctx->ev[2], ctx->st));
+    ctx->kev_n = 0;
     int launches = 0;
     if (ctx->full_tape) {
         hx::DevTape T{ctx->tv.p, ctx->tm.p, ctx->th.p, ctx->tn.p, 0};
+        if (hx_kev_mark(ctx, ctx->st)) return -1;
         HXC(bwd_launch(ctx, T, A, GR, PV, dLdv_dev, ctx->nstep, 0));
+        if (hx_kev_mark(ctx, ctx->st)) return -1;
         launches = 1;
     } else {
         for (int s = ctx->nseg - 1; s >= 0; s--) {
@@ -821,7 +837,9 @@ static int run_backward(hx_ctx* ctx, const double* dLdv_dev) {
             if (copy_ck(ctx, s, false)) return -1;
             hx::DevTape T{ctx->tv.p, ctx->tm.p, ctx->th.p, ctx->tn.p, k0};
             HXC(fwd_launch(ctx, S, T, 1, PV, nullptr, k0, k1));
+            if (hx_kev_mark(ctx, ctx->st)) return -1;
             HXC(bwd_launch(ctx, T, A, GR, PV, dLdv_dev, k1, k0));
+            if (hx_kev_mark(ctx, ctx->st)) return -1;
             launches += 2;
         }
     }
@@ -972,7 +990,19 @@ int hx_mse_loss_grad_dev(hx_ctx* ctx, const double* trace_dev, const double* tar
 }
 
 int hx_last_kernel_ms(hx_ctx* ctx, int which, double* ms, int* launches) {
-    if (!ctx || (which != 0 && which != 1)) return -1;
+    if (!ctx || which < 0 || which > 2) return -1;
+    if (which == 2) {  // the reverse kernel's launches alone
+        double sum = 0.0;
+        if (ctx->kev_n >= 2) HXC(cudaEventSynchronize(ctx->kev[ctx->kev_n - 1]));
+        for (int i = 0; i + 1 < ctx->kev_n; i += 2) {
+            float f = 0.f;
+            HXC(cudaEventElapsedTime(&f, ctx->kev[i], ctx->kev[i + 1]));
+            sum += f;
+        }
+        if (ms) *ms = sum;
+        if (launches) *launches = ctx->kev_n / 2;
+        return 0;
+    }
     HXC(cudaEventSynchronize(ctx->ev[which * 2 + 1]));
     float f = 0.f;
     HXC(cudaEventElapsedTime(&f, ctx->ev[which * 2], ctx->ev[which * 2 + 1]));
@@ -1064,10 +1094,22 @@ int hx_opt_grad_buffer(hx_ctx* ctx, int opt, double** dev_ptr, int* n) {
     return 0;
 }
 
+int hx_opt_set_allreduce(hx_ctx* ctx, int opt, hx_allreduce_fn fn, void* user) {
+    AdamOpt* o = get_opt(ctx, opt);
+    if (!o) return fail(ctx, "bad optimizer id");
+    o->allreduce = fn;
+    o->allreduce_user = user;
+    return 0;
+}
+
 int hx_opt_step(hx_ctx* ctx, int opt, double lr, double inv_record_steps) {
     AdamOpt* o = get_opt(ctx, opt);
     if (!o) return fail(ctx, "bad optimizer id");
     HXC(cudaSetDevice(ctx->device));
+    // data-parallel replicas: sum the slot gradients over ranks on the launch
+    // stream, ordered after the kernels that wrote them and before Adam
+    if (o->allreduce && o->allreduce(o->allreduce_user, o->grad.p, o->n, (void*)ctx->st) != 0)
+        return fail(ctx, "gradient all-reduce callback failed");
     o->step++;
     const double bc1 = std::pow(o->beta1, (double)o->step);
     const double bc2 = std::pow(o->beta2, (double)o->step);

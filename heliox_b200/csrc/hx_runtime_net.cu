@@ -408,41 +408,69 @@ int hx_net_forward(hx_ctx* ctx, int nstep, double v_init, double* trace_dev, boo
     const hx::Plan& P = ctx->P;
     const size_t nn = P.nnode;
     const int W = net_window(ctx, nstep);
-    if (net_netstim(ctx, nstep)) return -1;
-    if (capture && net_plan_tape(ctx, nstep, W)) return -1;
     const int ncell = (int)P.cs_node0.size();
-    ctx->win_cap = ncell * ((W + 1) / 2) + 1;
-    if (ctx->win_cap_user > 0) {  // all ranks must exchange buffers of one size
-        if (ctx->win_cap_user < ctx->win_cap)
-            return hx_fail(ctx, "exchange capacity below this group's bound of " + std::to_string(ctx->win_cap));
-        ctx->win_cap = ctx->win_cap_user;
-    }
+    // Several ranks exchange window spikes: every rank takes the same
+    // collective steps whatever happens locally.  A host-side failure on one
+    // rank does not end its loop early (its peers would wait in the next
+    // all-gather): it stops launching work, keeps exchanging (a send buffer
+    // of padding), and reports the failure in the status word all ranks
+    // all-gather after the last window; every rank then returns the same
+    // outcome, and a bucket overflow anywhere reruns the forward on all ranks
+    // with the largest bucket need.  Only a rank that cannot hold the
+    // exchange buffers, or whose exchange itself fails, returns at once (the
+    // process group's timeout then ends the peers' collective).
+    const bool multi = ctx->exchange && ctx->nranks > 1;
+    const int own_cap = ncell * ((W + 1) / 2) + 1;
+    ctx->win_cap = ctx->win_cap_user > 0 ? ctx->win_cap_user : own_cap;
     HXC(ctx->win_send.ensure(ctx->win_cap));
     HXC(ctx->win_recv.ensure((size_t)ctx->win_cap * std::max(ctx->nranks, 1)));
-    ctx->log_cap = (int)std::min<long long>((long long)ncell * std::max(64, nstep / 20 + 1), 1LL << 26);
-    HXC(ctx->spk_log.ensure(std::max(ctx->log_cap, 1)));
-    if (ctx->ev_cap == 0) ctx->ev_cap = ctx->nranks > 1 ? 1024 : 64;
-    HXC(ctx->ev_cnt.ensure(std::max(nstep, 1)));
+    if (multi) {
+        HXC(ctx->st_send.ensure(1));
+        HXC(ctx->st_recv.ensure((size_t)ctx->nranks));
+    }
+    auto setup = [&]() -> int {
+        if (ctx->win_cap < own_cap)  // all ranks must exchange buffers of one size
+            return hx_fail(ctx, "exchange capacity below this group's bound of " + std::to_string(own_cap));
+        if (net_netstim(ctx, nstep)) return -1;
+        if (capture && net_plan_tape(ctx, nstep, W)) return -1;
+        ctx->log_cap = (int)std::min<long long>((long long)ncell * std::max(64, nstep / 20 + 1), 1LL << 26);
+        HXC(ctx->spk_log.ensure(std::max(ctx->log_cap, 1)));
+        if (ctx->ev_cap == 0) ctx->ev_cap = ctx->nranks > 1 ? 1024 : 64;
+        HXC(ctx->ev_cnt.ensure(std::max(nstep, 1)));
+        return 0;
+    };
+    bool ok = setup() == 0;
+    if (!ok && !multi) return -1;
+    std::string local_err = ok ? std::string() : ctx->err;
     hx::DevProbe PV = hx_probe_view(ctx);
     const double half_dt = ctx->dt / 2;
     for (int attempt = 0; attempt < 6; attempt++) {
-        HXC(ctx->ev_syn.ensure((size_t)std::max(nstep, 1) * ctx->ev_cap));
-        HXC(cudaMemsetAsync(ctx->ev_cnt.p, 0, (size_t)std::max(nstep, 1) * 4, st));
-        HXC(cudaMemsetAsync(ctx->dev_err.p, 0, 4, st));
-        HXC(cudaMemsetAsync(ctx->log_n.p, 0, 4, st));
-        HXC(cudaMemsetAsync(ctx->cs_ps_flag.p, 0, (size_t)std::max(ncell, 1) * 4, st));
-        double* v0 = ctx->coupled ? ctx->vbuf.p : ctx->sv.p;
-        HXC(hx::launch_init(ctx->G, hx::DevState{v0, ctx->sm.p, ctx->sh.p, ctx->sn.p}, v_init, st));
-        HXC(hx::launch_init_net(ctx->nsyn, ctx->sA.p, ctx->sB.p, ctx->ngr, ctx->prm[HX_P_GRADED_W].p, ctx->gr_vth.p,
-                                ctx->gr_delta.p, ctx->gr_g.p, ctx->gr_k.p, ctx->gr_erev.p, ctx->gr_s.p, v_init, st));
-        if (attempt == 0) HXC(cudaEventRecord(ctx->ev[0], st));
-        if (ctx->nsyn && ctx->ns_count)
-            HXC(hx::launch_route(ctx->ns_spk.p, nullptr, ctx->ns_count, ctx->src_off.p, ctx->src_syn.p, ctx->nsrc,
-                                 ctx->syn_delay.p, ctx->tstart.p, nstep, half_dt, 0, ctx->ev_cnt.p, ctx->ev_syn.p,
-                                 ctx->ev_cap, ctx->dev_err.p, st));
+        if (ok && ctx->ev_syn.ensure((size_t)std::max(nstep, 1) * ctx->ev_cap) != cudaSuccess) {
+            hx_fail(ctx, "event bucket allocation failed");
+            if (!multi) return -1;
+            ok = false;
+            local_err = ctx->err;
+        }
+        auto init_attempt = [&]() -> int {
+            HXC(cudaMemsetAsync(ctx->ev_cnt.p, 0, (size_t)std::max(nstep, 1) * 4, st));
+            HXC(cudaMemsetAsync(ctx->dev_err.p, 0, 4, st));
+            HXC(cudaMemsetAsync(ctx->log_n.p, 0, 4, st));
+            HXC(cudaMemsetAsync(ctx->cs_ps_flag.p, 0, (size_t)std::max(ncell, 1) * 4, st));
+            double* v0 = ctx->coupled ? ctx->vbuf.p : ctx->sv.p;
+            HXC(hx::launch_init(ctx->G, hx::DevState{v0, ctx->sm.p, ctx->sh.p, ctx->sn.p}, v_init, st));
+            HXC(hx::launch_init_net(ctx->nsyn, ctx->sA.p, ctx->sB.p, ctx->ngr, ctx->prm[HX_P_GRADED_W].p,
+                                    ctx->gr_vth.p, ctx->gr_delta.p, ctx->gr_g.p, ctx->gr_k.p, ctx->gr_erev.p,
+                                    ctx->gr_s.p, v_init, st));
+            if (attempt == 0) HXC(cudaEventRecord(ctx->ev[0], st));
+            if (ctx->nsyn && ctx->ns_count)
+                HXC(hx::launch_route(ctx->ns_spk.p, nullptr, ctx->ns_count, ctx->src_off.p, ctx->src_syn.p,
+                                     ctx->nsrc, ctx->syn_delay.p, ctx->tstart.p, nstep, half_dt, 0, ctx->ev_cnt.p,
+                                     ctx->ev_syn.p, ctx->ev_cap, ctx->dev_err.p, st));
+            return 0;
+        };
         int launches = 0;
-        for (int k0 = 0; k0 < nstep; k0 += W) {
-            const int k1 = std::min(nstep, k0 + W);
+        // the window's compute: checkpoint, step kernel, spike log
+        auto run_window = [&](int k0, int k1) -> int {
             double* vin = ctx->coupled ? ctx->vbuf.p + (size_t)(k0 & 1) * nn : ctx->sv.p;
             if (capture && !ctx->full_tape && k0 % ctx->seg == 0)
                 if (net_ck(ctx, k0 / ctx->seg, true, vin)) return -1;
@@ -471,36 +499,83 @@ int hx_net_forward(hx_ctx* ctx, int nstep, double v_init, double* trace_dev, boo
             HXC(hx::launch_log_append(ctx->win_send.p, ctx->win_n.p, ctx->win_cap, ctx->spk_log.p, ctx->log_n.p,
                                       ctx->log_cap, ctx->dev_err.p, st));
             launches += 2;
-            if (ctx->exchange && ctx->nranks > 1) {
+            return 0;
+        };
+        auto route_window = [&](const int2* spk, const int* nspk, int nmax, int k1) -> int {
+            HXC(hx::launch_route(spk, nspk, nmax, ctx->src_off.p, ctx->src_syn.p, ctx->nsrc, ctx->syn_delay.p,
+                                 ctx->tstart.p, nstep, half_dt, k1, ctx->ev_cnt.p, ctx->ev_syn.p, ctx->ev_cap,
+                                 ctx->dev_err.p, st));
+            launches++;
+            return 0;
+        };
+        if (ok && init_attempt() != 0) {
+            if (!multi) return -1;
+            ok = false;
+            local_err = ctx->err;
+        }
+        for (int k0 = 0; k0 < nstep; k0 += W) {
+            const int k1 = std::min(nstep, k0 + W);
+            if (ok && run_window(k0, k1) != 0) {
+                if (!multi) return -1;
+                ok = false;
+                local_err = ctx->err;
+            }
+            if (multi) {
+                if (!ok)  // stopped: keep the collective going with an empty window
+                    cudaMemsetAsync(ctx->win_send.p, 0xFF, (size_t)ctx->win_cap * sizeof(int2), st);
                 if (ctx->exchange(ctx->exchange_user, ctx->win_send.p, ctx->win_recv.p, ctx->win_cap, (void*)st) != 0)
                     return hx_fail(ctx, "spike exchange callback failed");
-                if (ctx->nsyn)
-                    HXC(hx::launch_route(ctx->win_recv.p, nullptr, ctx->win_cap * ctx->nranks, ctx->src_off.p,
-                                         ctx->src_syn.p, ctx->nsrc, ctx->syn_delay.p, ctx->tstart.p, nstep, half_dt,
-                                         k1, ctx->ev_cnt.p, ctx->ev_syn.p, ctx->ev_cap, ctx->dev_err.p, st));
+                if (ok && ctx->nsyn && route_window(ctx->win_recv.p, nullptr, ctx->win_cap * ctx->nranks, k1) != 0) {
+                    ok = false;
+                    local_err = ctx->err;
+                }
             } else if (ctx->nsyn && k1 < nstep) {
-                HXC(hx::launch_route(ctx->win_send.p, ctx->win_n.p, ctx->win_cap, ctx->src_off.p, ctx->src_syn.p,
-                                     ctx->nsrc, ctx->syn_delay.p, ctx->tstart.p, nstep, half_dt, k1, ctx->ev_cnt.p,
-                                     ctx->ev_syn.p, ctx->ev_cap, ctx->dev_err.p, st));
-                launches++;
+                if (route_window(ctx->win_send.p, ctx->win_n.p, ctx->win_cap, k1) != 0) return -1;
             }
         }
-        if (ctx->coupled) {  // final voltages into the state vector
+        if (ok && ctx->coupled) {  // final voltages into the state vector
             HXC(cudaMemcpyAsync(ctx->sv.p, ctx->vbuf.p + (size_t)(nstep & 1) * nn, nn * 8, cudaMemcpyDeviceToDevice,
                                 st));
         }
-        HXC(cudaEventRecord(ctx->ev[1], st));
-        int err = 0;
-        HXC(cudaMemcpyAsync(&err, ctx->dev_err.p, 4, cudaMemcpyDeviceToHost, st));
-        HXC(cudaStreamSynchronize(st));
-        ctx->launches[0] = launches;
-        if (err & 1) return hx_fail(ctx, "an event fell inside a simulated window (window longer than the delay)");
-        if (err & 4) return hx_fail(ctx, "window spike buffer overflow");
-        if (err & 2) {
-            if (ctx->nranks > 1) return hx_fail(ctx, "event bucket overflow (raise the per-step capacity)");
-            std::vector<int> cnt(std::max(nstep, 1));
-            HXC(cudaMemcpy(cnt.data(), ctx->ev_cnt.p, cnt.size() * 4, cudaMemcpyDeviceToHost));
-            int need = *std::max_element(cnt.begin(), cnt.end());
+        int err = 0, need = 0, bad_rank = -1;
+        if (multi) {
+            // every rank's (error bits, largest bucket count) after its last window
+            if (ok && hx::launch_net_status(ctx->dev_err.p, ctx->ev_cnt.p, nstep, 0, ctx->st_send.p, st) !=
+                          cudaSuccess) {
+                ok = false;
+                local_err = "status kernel launch failed";
+            }
+            if (!ok) {  // a stopped rank reports only that it stopped
+                const int2 ab = make_int2(HX_XS_ABORT, 0);
+                cudaMemcpyAsync(ctx->st_send.p, &ab, sizeof(int2), cudaMemcpyHostToDevice, st);
+            }
+            if (ctx->exchange(ctx->exchange_user, ctx->st_send.p, ctx->st_recv.p, 1, (void*)st) != 0)
+                return hx_fail(ctx, "spike exchange callback failed (status)");
+            std::vector<int2> all(ctx->nranks);
+            HXC(cudaMemcpyAsync(all.data(), ctx->st_recv.p, all.size() * sizeof(int2), cudaMemcpyDeviceToHost, st));
+            HXC(cudaEventRecord(ctx->ev[1], st));
+            HXC(cudaStreamSynchronize(st));
+            hx_exchange_merge_status(reinterpret_cast<const int*>(all.data()), ctx->nranks, &err, &need, &bad_rank);
+            if (err & HX_XS_ABORT)
+                return hx_fail(ctx, local_err.empty()
+                                        ? "rank " + std::to_string(bad_rank) + " failed in the multi-rank forward"
+                                        : local_err);
+        } else {
+            HXC(cudaEventRecord(ctx->ev[1], st));
+            HXC(cudaMemcpyAsync(&err, ctx->dev_err.p, 4, cudaMemcpyDeviceToHost, st));
+            HXC(cudaStreamSynchronize(st));
+        }
+        ctx->launches[0] = launches + (multi ? 1 : 0);
+        if (err & HX_XS_LATE_EVENT)
+            return hx_fail(ctx, "an event fell inside a simulated window (window longer than the delay)");
+        if (err & HX_XS_WINDOW) return hx_fail(ctx, "window spike buffer overflow");
+        if (err & HX_XS_BUCKET) {
+            if (!multi) {
+                std::vector<int> cnt(std::max(nstep, 1));
+                HXC(cudaMemcpy(cnt.data(), ctx->ev_cnt.p, cnt.size() * 4, cudaMemcpyDeviceToHost));
+                need = *std::max_element(cnt.begin(), cnt.end());
+            }
+            // every rank takes the same (largest) need, so all rerun alike
             ctx->ev_cap = std::max(ctx->ev_cap * 2, need + need / 4 + 8);
             continue;  // the run depended on dropped events: run it again with room for all
         }
@@ -554,17 +629,20 @@ int hx_net_backward(hx_ctx* ctx, const double* dLdv_dev) {
         N.x_gr_out = out + ctx->nhg + ctx->ngj;
     };
     auto sweep = [&](int k_hi, int k_lo, const hx::DevTape& T) -> int {
+        if (hx_kev_mark(ctx, st)) return -1;
         if (!ctx->coupled) {
             HXC(hx::launch_bwd(ctx->G, T, A, GR, PV, dLdv_dev, ctx->tmid.p, k_hi, k_lo, st, &N));
-            return 1;
+        } else {
+            for (int k = k_hi - 1; k >= k_lo; --k) {
+                set_x(k);
+                HXC(hx::launch_bwd(ctx->G, T, A, GR, PV, dLdv_dev, ctx->tmid.p, k + 1, k, st, &N));
+            }
         }
-        for (int k = k_hi - 1; k >= k_lo; --k) {
-            set_x(k);
-            HXC(hx::launch_bwd(ctx->G, T, A, GR, PV, dLdv_dev, ctx->tmid.p, k + 1, k, st, &N));
-        }
-        return k_hi - k_lo;
+        if (hx_kev_mark(ctx, st)) return -1;
+        return ctx->coupled ? k_hi - k_lo : 1;
     };
     HXC(cudaEventRecord(ctx->ev[2], st));
+    ctx->kev_n = 0;
     int launches = 0;
     if (ctx->full_tape) {
         hx::DevTape T{ctx->tv.p, ctx->tm.p, ctx->th.p, ctx->tn.p, 0};
@@ -668,6 +746,22 @@ int hx_set_exchange(hx_ctx* ctx, hx_exchange_fn exchange, void* user, int nranks
     ctx->nranks = exchange ? nranks : 1;
     ctx->win_cap_user = exchange ? cap_entries : 0;
     ctx->ev_cap = 0;
+    return 0;
+}
+
+int hx_exchange_merge_status(const int* status, int nranks, int* flags, int* need, int* first_rank) {
+    if (!status || nranks < 1 || !flags || !need || !first_rank) return -1;
+    int f = 0, nd = 0, hard = -1, soft = -1;
+    for (int r = 0; r < nranks; r++) {
+        const int b = status[2 * r], q = status[2 * r + 1];
+        f |= b;
+        nd = std::max(nd, q);
+        if ((b & ~HX_XS_BUCKET) && hard < 0) hard = r;
+        if ((b & HX_XS_BUCKET) && soft < 0) soft = r;
+    }
+    *flags = f;
+    *need = nd;
+    *first_rank = hard >= 0 ? hard : soft;
     return 0;
 }
 

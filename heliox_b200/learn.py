@@ -159,29 +159,30 @@ def mse_objective(trace: np.ndarray, target: np.ndarray) -> Tuple[float, np.ndar
 
 def train_adam(runtime: AdjointRuntime, handles: Sequence[int], target: np.ndarray, epochs: int,
                lr: float = 1e-3, probes: Optional[Sequence[int]] = None, total_steps: Optional[int] = None,
-               allreduce: Optional[Callable[[int, int], None]] = None,
+               allreduce: Optional[Callable[[int, int, int], None]] = None,
                on_epoch: Optional[Callable[[int, float], None]] = None) -> List[float]:
     """Fit the parameters behind ``handles`` to ``target`` with the device Adam.
 
     Each epoch: forward capture, MSE against ``target`` on the host, reverse
     sweep, gradients of the bound parameters copied into the optimizer's slots
-    on the device (optionally all-reduced across ranks by ``allreduce(ptr, n)``),
-    one Adam step.  Returns the loss history.
+    on the device, one Adam step.  With data-parallel replicas (one trial or
+    teacher per rank) ``allreduce`` is the optimizer's all-reduce hook
+    (``shard.allreduce_sum()``): each step first sums the slot gradients over
+    the ranks on the library's stream.  Returns the loss history.
     """
     sim = runtime.sim
     probes = runtime.group.soma_nodes() if probes is None else np.asarray(probes, dtype=np.int32)
     T = int(total_steps if total_steps is not None else target.shape[0] - 1)
     opt = sim.create_optimizer("adam")
     sim.optimizer_add_external_grads(opt, list(handles), impedance=1.0)
+    if allreduce is not None:
+        sim.optimizer_set_allreduce(opt, allreduce)
     hist = []
     for ep in range(int(epochs)):
         tr = sim.forward_capture(T, probes=probes)
         loss, g = mse_objective(tr, target)
         sim.backward(g, keys=())
         sim.optimizer_grads_from_backward(opt)
-        if allreduce is not None:
-            ptr, n = sim.optimizer_grad_buffer(opt)
-            allreduce(ptr, n)
         sim.optimizer_step_with_inv_record_steps(opt, lr, 1.0)
         hist.append(loss)
         if on_epoch:

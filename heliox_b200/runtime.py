@@ -96,6 +96,7 @@ class Sim:
         self._nstep = None
         self._probes = None
         self._opt_hyper: Dict[int, tuple] = {}
+        self._arfn: Dict[int, object] = {}  # ctypes callbacks of the optimizers' all-reduce hooks
 
     # ------------------------------------------------------------------ basics
     def _check(self, rc: int, what: str):
@@ -399,6 +400,31 @@ class Sim:
         n = C.c_int(0)
         self._check(self._L.hx_opt_grad_buffer(self._ctx, int(opt), C.byref(ptr), C.byref(n)), "hx_opt_grad_buffer")
         return int(ptr.value or 0), int(n.value)
+
+    def optimizer_set_allreduce(self, opt: int, fn):
+        """Install the data-parallel gradient all-reduce of optimizer ``opt``:
+        ``fn(grad_ptr, n, stream_ptr)`` must replace the n fp64 slot gradients
+        at ``grad_ptr`` by their sum over ranks on the given stream
+        (``shard.allreduce_sum``); each step calls it before Adam.  ``None``
+        removes it."""
+        if fn is None:
+            self._arfn.pop(opt, None)
+            self._check(self._L.hx_opt_set_allreduce(self._ctx, int(opt), _lib.ALLREDUCE_FN(), None),
+                        "hx_opt_set_allreduce")
+            return
+
+        def cb(user, grad, n, stream):
+            try:
+                fn(int(grad or 0), int(n), int(stream or 0))
+                return 0
+            except Exception:  # an exception must not cross the C boundary
+                import traceback
+
+                traceback.print_exc()
+                return -1
+
+        self._arfn[opt] = _lib.ALLREDUCE_FN(cb)
+        self._check(self._L.hx_opt_set_allreduce(self._ctx, int(opt), self._arfn[opt], None), "hx_opt_set_allreduce")
 
     def optimizer_step_with_inv_record_steps(self, opt: int, learning_rate: float, inv_record_steps: float = 1.0):
         self._check(self._L.hx_opt_step(self._ctx, int(opt), float(learning_rate), float(inv_record_steps)),

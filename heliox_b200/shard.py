@@ -124,28 +124,93 @@ def exchange_capacity(g: CellGroup, nranks: int, window: int) -> int:
     return most * ((window + 1) // 2) + 1
 
 
-def allgather_exchange(group=None):
+class _DevView:
+    """A device buffer (pointer, count, numpy type string) seen by torch without a copy."""
+
+    def __init__(self, ptr: int, n: int, typestr: str):
+        self.__cuda_array_interface__ = {"shape": (n,), "typestr": typestr, "data": (ptr, False), "version": 3}
+
+
+def _wrap(ptr: int, n: int, ctype, device: str):
+    """torch view of n elements at ``ptr``: device memory ("cuda") or host memory
+    ("cpu", for hooks tested with the gloo backend)."""
+    import ctypes as C
+
+    import torch
+
+    if device == "cpu":
+        arr = np.ctypeslib.as_array(C.cast(ptr, C.POINTER(ctype)), shape=(n,))
+        return torch.from_numpy(arr)
+    typestr = {C.c_int: "<i4", C.c_double: "<f8"}[ctype]
+    return torch.as_tensor(_DevView(ptr, n, typestr), device="cuda")
+
+
+def _on_stream(stream_ptr: int, device: str):
+    """Context that makes the library's launch stream torch's current stream, so
+    the collective is ordered after the kernels that wrote its input and before
+    the ones that read its output, whatever stream the caller had current."""
+    import contextlib
+
+    import torch
+
+    if device != "cuda" or not stream_ptr:
+        return contextlib.nullcontext()
+    return torch.cuda.stream(torch.cuda.ExternalStream(stream_ptr))
+
+
+def allgather_exchange(group=None, device: str = "cuda"):
     """Exchange hook for ``Sim.set_exchange`` over ``torch.distributed``.
 
-    The library hands over device pointers (its window send buffer and a
-    receive buffer of nranks times its size); the hook wraps them as CUDA
-    tensors without copying and all-gathers on the current stream, which must
-    be the library's launch stream (``Sim.set_stream``).
+    The library hands over its window send buffer and a receive buffer of
+    nranks times its size (``cap`` (gid, step) int32 pairs per rank; ``cap`` is
+    1 for the status pair after the last window) and its launch stream; the
+    hook wraps the buffers without copying and all-gathers on that stream.
+    ``device="cpu"`` takes host buffers (gloo tests of the protocol).
     """
-    import torch
-    import torch.distributed as dist
+    import ctypes as C
 
-    class _View:
-        def __init__(self, ptr: int, n: int):
-            self.__cuda_array_interface__ = {"shape": (n,), "typestr": "<i4", "data": (ptr, False), "version": 3}
+    import torch.distributed as dist
 
     def fn(send_ptr: int, recv_ptr: int, cap: int, stream_ptr: int) -> None:
         ws = dist.get_world_size(group)
-        send = torch.as_tensor(_View(send_ptr, 2 * cap), device="cuda")
-        recv = torch.as_tensor(_View(recv_ptr, 2 * cap * ws), device="cuda")
-        dist.all_gather_into_tensor(recv, send, group=group)
+        send = _wrap(send_ptr, 2 * cap, C.c_int, device)
+        recv = _wrap(recv_ptr, 2 * cap * ws, C.c_int, device)
+        with _on_stream(stream_ptr, device):
+            dist.all_gather_into_tensor(recv, send, group=group)
 
     return fn
+
+
+def allreduce_sum(group=None, device: str = "cuda"):
+    """Gradient hook for ``Sim.optimizer_set_allreduce``: the optimizer's n fp64
+    slot gradients are summed over the ranks of ``group`` in place, on the
+    library's launch stream, before every Adam step (data-parallel replicas,
+    e.g. one trial or teacher per GPU)."""
+    import ctypes as C
+
+    import torch.distributed as dist
+
+    def fn(grad_ptr: int, n: int, stream_ptr: int) -> None:
+        g = _wrap(grad_ptr, n, C.c_double, device)
+        with _on_stream(stream_ptr, device):
+            dist.all_reduce(g, op=dist.ReduceOp.SUM, group=group)
+
+    return fn
+
+
+def merge_status(status: np.ndarray) -> Tuple[int, int, int]:
+    """(flags, need, first_rank) of the gathered per-rank status pairs, by the
+    library's own rule (``hx_exchange_merge_status``; host only)."""
+    import ctypes as C
+
+    from . import _lib
+
+    L = _lib.load()
+    st = np.ascontiguousarray(status, dtype=np.int32).reshape(-1)
+    f, nd, r = C.c_int(0), C.c_int(0), C.c_int(0)
+    if L.hx_exchange_merge_status(_lib.iptr(st), st.shape[0] // 2, C.byref(f), C.byref(nd), C.byref(r)) != 0:
+        raise ValueError("bad status array")
+    return int(f.value), int(nd.value), int(r.value)
 
 
 def pad_spikes(gid: np.ndarray, step: np.ndarray, cap: int) -> np.ndarray:

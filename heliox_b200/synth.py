@@ -510,48 +510,67 @@ def network_config4(ncell: int = 10000, seed: int = 4, syn_per_cell: int = 100, 
                                  rate_hz=rate_hz)
 
 
-def network_config4_shard(ncell: int, rank: int, nranks: int, seed: int = 4, syn_per_cell: int = 100,
-                          nmin: int = 400, nmax: int = 600, rate_hz: float = 5.0) -> CellGroup:
-    """Rank ``rank``'s part of a config-4 network of ``nranks * ncell`` cells.
+def config4_cell_range(total: int, rank: int, nranks: int) -> Tuple[int, int]:
+    """Cells [c0, c1) of rank ``rank``: contiguous, counts differing by at most one."""
+    return total * rank // nranks, total * (rank + 1) // nranks
 
-    Built directly per rank (no rank needs the others' cells): cells
-    ``rank*ncell .. (rank+1)*ncell - 1`` seeded by their global id, their
-    synapses with global NetCon sources drawn over all cells, and the whole
-    NetStim table (one per global cell).  ``meta`` records ``gid_base`` and
-    ``nsrc_cells`` for ``Sim.load_group``.
+
+def network_config4_shard(total: int, rank: int, nranks: int, seed: int = 4, syn_per_cell: int = 100,
+                          nmin: int = 400, nmax: int = 600, rate_hz: float = 5.0,
+                          teacher_sigma: float = 0.2) -> CellGroup:
+    """Rank ``rank``'s part of the config-4 network of ``total`` cells.
+
+    The network does not depend on how it is split: cell c (global id) has
+    its morphology seeded by c, and its synapses -- location, presynaptic
+    source over all ``total`` cells, sign, delay, weight, plus the synapse of
+    its NetStim -- drawn from a generator seeded by (seed, c).  Rank r builds
+    only its cells ``config4_cell_range(total, r, nranks)`` with their
+    synapses (global NetCon sources) and the whole NetStim table (one per
+    global cell, ids total + c).  ``meta`` records ``gid_base``,
+    ``nsrc_cells`` and ``teacher_weight``: the weights lognormally perturbed
+    (sigma ``teacher_sigma``, generator seeded by (seed, 7, c)) in the
+    group's synapse order, the teacher network of the loss.
     """
-    total = ncell * nranks
-    base = rank * ncell
-    cells = [random_tree_cell(seed * 100000 + base + c, nmin=nmin, nmax=nmax) for c in range(ncell)]
-    g = concat_groups(cells, name=f"net{total}.r{rank}")
-    rng = np.random.default_rng([seed, rank])
+    c0, c1 = config4_cell_range(total, rank, nranks)
+    ncell = c1 - c0
+    cells = [random_tree_cell(seed * 100000 + c, nmin=nmin, nmax=nmax) for c in range(c0, c1)]
+    g = concat_groups(cells, name=f"net{total}.r{rank}of{nranks}")
     cell = g.cell_of_node()
     order = np.argsort(cell, kind="stable")
     bounds = np.searchsorted(cell[order], np.arange(ncell + 1))
-    nsyn = ncell * syn_per_cell
-    post = np.repeat(np.arange(ncell), syn_per_cell)
-    pick = bounds[post] + (rng.random(nsyn) * (bounds[post + 1] - bounds[post])).astype(np.int64)
-    nodes = order[pick]
-    src = rng.integers(0, total - 1, nsyn)
-    src = np.where(src >= post + base, src + 1, src)  # no self-connection
-    exc = rng.random(nsyn) < 0.8
-    e = np.where(exc, 0.0, -80.0)
-    d = rng.uniform(1.0, 5.0, nsyn)
-    w = np.exp(rng.normal(-7.0, 1.0, nsyn))
-    # the NetStim of every local cell drives one more synapse at its soma
-    nodes = np.concatenate([nodes, np.arange(ncell)])
-    src = np.concatenate([src, total + base + np.arange(ncell)])
-    e = np.concatenate([e, np.zeros(ncell)])
-    d = np.concatenate([d, rng.uniform(1.0, 5.0, ncell)])
-    w = np.concatenate([w, np.full(ncell, 0.01)])
+    k = syn_per_cell
+    nodes = np.empty(ncell * (k + 1), np.int64)
+    src = np.empty_like(nodes)
+    e = np.empty(nodes.shape[0])
+    d = np.empty_like(e)
+    w = np.empty_like(e)
+    wt = np.empty_like(e)
+    for i in range(ncell):
+        gc = c0 + i
+        rng = np.random.default_rng([seed, gc])
+        sl = slice(i * (k + 1), (i + 1) * (k + 1))
+        nloc = bounds[i + 1] - bounds[i]
+        pick = bounds[i] + (rng.random(k) * nloc).astype(np.int64)
+        s = rng.integers(0, total - 1, k)
+        s = np.where(s >= gc, s + 1, s)  # no self-connection
+        exc = rng.random(k) < 0.8
+        # synapses of cell gc, then the one its NetStim drives at the soma
+        nodes[sl] = np.concatenate([order[pick], [i]])
+        src[sl] = np.concatenate([s, [total + gc]])
+        e[sl] = np.concatenate([np.where(exc, 0.0, -80.0), [0.0]])
+        d[sl] = rng.uniform(1.0, 5.0, k + 1)
+        w[sl] = np.concatenate([np.exp(rng.normal(-7.0, 1.0, k)), [0.01]])
+        wt[sl] = w[sl] * np.exp(teacher_sigma * np.random.default_rng([seed, 7, gc]).standard_normal(k + 1))
     n = nodes.shape[0]
+    o = np.argsort(nodes, kind="stable")  # the table order _table gives
     g.exp2syn = _table(nodes, {"tau1": np.full(n, 0.5), "tau2": np.full(n, 5.0), "e": e, "delay": d, "weight": w},
                        {"src": src})
     g.netstim = MechTable(_i32(np.zeros(total)), {
         "interval": _f64(np.full(total, 1000.0 / rate_hz)), "number": _f64(np.full(total, 1e9)),
         "start": _f64(np.zeros(total)), "noise": _f64(np.ones(total))})
-    g.meta["gid_base"] = base
+    g.meta["gid_base"] = c0
     g.meta["nsrc_cells"] = total
+    g.meta["teacher_weight"] = _f64(wt[o])
     g.validate()
     return g
 

@@ -372,8 +372,27 @@ int hx_netstim_trains(const hx_group_desc* desc, int nstep, int cap, int* id, in
 typedef int (*hx_exchange_fn)(void* user, const void* send_dev, void* recv_dev, int cap_entries, void* stream);
 /* cap_entries: the window buffer size, identical on every rank and at least
  * (this group's cells) * ceil(window / 2) (a PreSyn fires at most every other
- * step); pass the maximum over ranks.  0 = this group's own bound (one rank). */
+ * step); pass the maximum over ranks.  0 = this group's own bound (one rank).
+ * The hook is called once per window with cap_entries and, after the last
+ * window, once more with cap_entries = 1: every rank's status pair
+ * (HX_XS_* bits, largest event-bucket count) is all-gathered, so that all
+ * ranks return the same outcome (a rank whose host work failed keeps
+ * exchanging empty windows until then and reports HX_XS_ABORT; a bucket
+ * overflow on any rank reruns the forward on every rank).  A hook that
+ * returns nonzero ends the forward on that rank at once; its peers' next
+ * collective then ends by the process group's timeout. */
 int hx_set_exchange(hx_ctx* ctx, hx_exchange_fn exchange, void* user, int nranks, int cap_entries);
+/* Status bits of a rank after the last window of a multi-rank forward. */
+#define HX_XS_LATE_EVENT 1 /* an event fell inside an already simulated window */
+#define HX_XS_BUCKET 2     /* a per-step event bucket overflowed (the forward is rerun) */
+#define HX_XS_WINDOW 4     /* the window spike buffer overflowed */
+#define HX_XS_ABORT 8      /* the rank's host work failed; it only kept exchanging */
+/* Merge of the gathered status pairs (status[2 r] bits, status[2 r + 1]
+ * bucket need of rank r): *flags = OR of the bits, *need = the largest need,
+ * *first_rank = the lowest rank with a bit other than HX_XS_BUCKET set (else
+ * the lowest with HX_XS_BUCKET, else -1).  Host only; the rule every rank
+ * applies, exposed for hosts that drive their own exchange. */
+int hx_exchange_merge_status(const int* status, int nranks, int* flags, int* need, int* first_rank);
 /* Steps per forward window of an event network (0 = derived from the smallest
  * NetCon delay of this group); returns the effective value with hx_get_window. */
 int hx_set_window(hx_ctx* ctx, int steps);
@@ -430,6 +449,15 @@ int hx_opt_set_grads_f32(hx_ctx* ctx, int opt, const float* grads, int n);
 int hx_opt_grads_from_backward(hx_ctx* ctx, int opt, double scale);
 /* Device pointer and length of the slot gradients (e.g. for an all-reduce before hx_opt_step). */
 int hx_opt_grad_buffer(hx_ctx* ctx, int opt, double** dev_ptr, int* n);
+/* Data-parallel replicas (e.g. one trial or teacher per GPU): hx_opt_step
+ * first calls allreduce(user, grad_dev, n, stream), which must replace the n
+ * fp64 slot gradients at grad_dev by their sum over all ranks (an in-place
+ * ncclAllReduce on `stream`) before it returns; then every rank applies the
+ * same Adam update.  NULL removes the hook.  The reference has one process
+ * and no collective; its Adam (src/optimizer/optimizer.cpp:351-397) receives
+ * the summed gradient here. */
+typedef int (*hx_allreduce_fn)(void* user, double* grad_dev, int n, void* stream);
+int hx_opt_set_allreduce(hx_ctx* ctx, int opt, hx_allreduce_fn fn, void* user);
 int hx_opt_step(hx_ctx* ctx, int opt, double lr, double inv_record_steps);
 /* hyper3 = {beta1, beta2, eps}; optimizer_get/set_adam_state (SimWrapper.cpp:419-451). */
 int hx_opt_get_adam_state(hx_ctx* ctx, int opt, long long* step, double* m, double* v, int n, double* hyper3);
@@ -465,7 +493,9 @@ int hx_mse_loss_grad_noalloc(const double* trace_dev, const double* target_dev, 
 
 /* ---- timing (CUDA events on the launch stream) ---------------------------------- */
 /* Milliseconds of the last forward-capture / backward kernel work, measured with
- * events recorded around the launches.  which: 0 forward, 1 backward. */
+ * events recorded around the launches.  which: 0 forward, 1 backward (with the
+ * recompute of checkpointed segments), 2 the reverse kernel's launches alone
+ * (summed; *launches = their count). */
 int hx_last_kernel_ms(hx_ctx* ctx, int which, double* ms, int* launches);
 
 #ifdef __cplusplus

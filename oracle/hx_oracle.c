@@ -28,11 +28,13 @@
  * discrete; their times do not move under an infinitesimal parameter change
  * that crosses no threshold).
  */
+#define _POSIX_C_SOURCE 199309L /* clock_gettime under -std=c11 */
 #include "hx_oracle.h"
 #include "hx_oracle_lib.h"
 
 #include <math.h>
 #include <stdint.h>
+#include <time.h>
 #include <stdlib.h>
 #include <string.h>
 
@@ -806,6 +808,10 @@ static void zero_if(double* p, int n) {
         if (gr && gr->arr) gr->arr[j] += (x); \
     } while (0)
 
+static _Thread_local double g_last_reverse_s = 0.0;
+
+double hxo_last_reverse_seconds(void) { return g_last_reverse_s; }
+
 int hxo_adjoint(const hxo_group* g, double v_init, int nstep, int nprobe, const int* probe, const double* dLdv,
                 double* trace, hxo_grads* gr) {
     if (g->lib) return -2; /* library mechanisms: gradients are checked by finite differences */
@@ -874,6 +880,9 @@ int hxo_adjoint(const hxo_group* g, double v_init, int nstep, int nprobe, const 
         if (trace) record(g, &s, nprobe, probe, trace + (size_t)(k + 1) * nprobe);
     }
     memcpy(tv + (size_t)nstep * nn, s.v, sizeof(double) * nn);
+    /* the reverse sweep's own wall time starts here (hxo_last_reverse_seconds) */
+    struct timespec t_rev0;
+    clock_gettime(CLOCK_MONOTONIC, &t_rev0);
     /* deliveries grouped by step (recorded in step order) */
     for (int e = 0; e < s.nev; e++) ev_off[s.ev[2 * e] + 1]++;
     for (int k = 0; k < nstep + 1; k++) ev_off[k + 1] += ev_off[k];
@@ -1059,6 +1068,11 @@ int hxo_adjoint(const hxo_group* g, double v_init, int nstep, int nprobe, const 
             lv[i] += g->b[i] * w[i] - g->a[i] * w[p];
             lv[p] += g->a[i] * w[p] - g->b[i] * w[i];
         }
+    }
+    {
+        struct timespec t_rev1;
+        clock_gettime(CLOCK_MONOTONIC, &t_rev1);
+        g_last_reverse_s = (double)(t_rev1.tv_sec - t_rev0.tv_sec) + 1e-9 * (double)(t_rev1.tv_nsec - t_rev0.tv_nsec);
     }
     rc = 0;
 done:

@@ -141,6 +141,9 @@ int hxo_forward_lib(const hxo_group* g, double v_init, int nstep, int nprobe, co
  * the forward is written to trace (may be NULL). */
 int hxo_adjoint(const hxo_group* g, double v_init, int nstep, int nprobe, const int* probe,
                 const double* dLdv, double* trace, hxo_grads* grads);
+/* Wall time (s) of the reverse sweep of this thread's last hxo_adjoint call
+ * (after its taped forward), for the CPU baseline's timing. */
+double hxo_last_reverse_seconds(void);
 
 #ifdef __cplusplus
 }

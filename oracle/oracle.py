@@ -103,12 +103,15 @@ def ref_available() -> bool:
 
 
 def ref_forward(g, nstep: int, probe: Optional[Sequence[int]] = None, v_init: Optional[float] = None,
-                workdir: Optional[str] = None):
+                workdir: Optional[str] = None, permute_type: int = 0, timing: bool = False):
     """Run the reference's own CPU integrator (oracle/_ref/hxref_run) on ``g``.
 
     The group is exported in CoreNEURON format (heliox_b200.coredat) and loaded
-    by the reference's read_coredat/data_format_trans; returns
-    (trace[(nstep+1), nprobe], spikes list of (t, gid)).
+    by the reference's read_coredat/data_format_trans with node permutation
+    ``permute_type`` (0, 1 or 3); returns (trace[(nstep+1), nprobe], spikes
+    list of (t, gid)), plus, with ``timing``, the seconds the reference spent
+    in finitialize and its fadvance loop (measured inside the harness:
+    loading, export and output are not counted).
     """
     import shutil
     import tempfile
@@ -127,8 +130,8 @@ def ref_forward(g, nstep: int, probe: Optional[Sequence[int]] = None, v_init: Op
         tf = os.path.join(tmp, "trace.f64")
         spk = os.path.join(tmp, "spk")
         vi = float(g.v_init if v_init is None else v_init)
-        r = subprocess.run([REF_LIB, data, "0", repr(float(g.dt)), str(int(nstep)), repr(vi), pf, tf, spk],
-                           capture_output=True, text=True)
+        r = subprocess.run([REF_LIB, data, str(int(permute_type)), repr(float(g.dt)), str(int(nstep)), repr(vi), pf,
+                            tf, spk], capture_output=True, text=True)
         if r.returncode != 0:
             raise RuntimeError(f"reference run failed ({r.returncode}):\n{r.stdout[-2000:]}\n{r.stderr[-2000:]}")
         trace = np.fromfile(tf, dtype=np.float64).reshape(nstep + 1, probe.shape[0])
@@ -138,6 +141,9 @@ def ref_forward(g, nstep: int, probe: Optional[Sequence[int]] = None, v_init: Op
             for line in open(sf):
                 t, gid = line.split()
                 spikes.append((float(t), int(gid)))
+        if timing:
+            secs = [float(line.split()[1]) for line in r.stdout.splitlines() if line.startswith("HXREF_FADVANCE_S")]
+            return trace, spikes, secs[-1]
         return trace, spikes
     finally:
         shutil.rmtree(tmp, ignore_errors=True)
@@ -204,6 +210,8 @@ def lib():
         L.hxo_adjoint.restype = C.c_int
         L.hxo_forward_lib.argtypes = [C.POINTER(_Group), C.c_double, C.c_int, C.c_int, _ip, _dp, _dp, C.c_int]
         L.hxo_forward_lib.restype = C.c_int
+        L.hxo_last_reverse_seconds.argtypes = []
+        L.hxo_last_reverse_seconds.restype = C.c_double
         _LIB = L
     return _LIB
 
@@ -361,7 +369,8 @@ NET_GRAD_KEYS = ("ExpSyn.weight", "ExpSyn.e", "Exp2Syn.weight", "Exp2Syn.e", "Ha
 
 
 def adjoint(g, nstep: int, dLdv: np.ndarray, probe: Optional[Sequence[int]] = None, v_init: Optional[float] = None):
-    """Forward + reverse sweep; returns (trace, grads dict keyed by GRAD_KEYS)."""
+    """Forward + reverse sweep; returns (trace, grads dict keyed by GRAD_KEYS).
+    ``grads["reverse_s"]`` is the wall time of the reverse sweep alone."""
     L = lib()
     probe = np.ascontiguousarray(g.soma_nodes() if probe is None else probe, dtype=np.int32)
     dLdv = np.ascontiguousarray(dLdv, dtype=np.float64)
@@ -395,4 +404,5 @@ def adjoint(g, nstep: int, dLdv: np.ndarray, probe: Optional[Sequence[int]] = No
         raise RuntimeError("oracle adjoint failed")
     if g.has_network:
         out["spikes"] = b.spikes()
+    out["reverse_s"] = float(L.hxo_last_reverse_seconds())
     return trace, out

@@ -9,13 +9,22 @@
 // Simulate(CPU), data_format_trans, finitialize, then fadvance per step (the
 // trace is read from the group's voltage vector after every step, like
 // LearnRuntime::simulate_output_vs_into), and output_spikes into spike_dir.
-// Only permute type 0 (the reference's CPU default, src/main.cpp:149-152) is
-// used, so reference node i is the group's node i.
+// permute_type 0 (the reference's CPU default, src/main.cpp:149-152) keeps
+// node i of the files at group node i; types 1 and 3 (the reference's
+// default in python_lib/heliox_learn/runtime.py:13) let read_coredat permute
+// the nodes (src/io/read_coredat.cpp:825-875, permute_order.cpp:145-210) and
+// solve with cpu_solve_permute1 / cpu_solve_permute3 (src/simulate.cpp:
+// 583-713); probes are then read at the permuted index (the group's
+// permute[i] is where file node i went).  HalfGap wiring is supported for
+// type 0 only.  The wall time of finitialize plus the fadvance loop (the
+// reference's integration alone, without loading or output) is printed as
+// "HXREF_FADVANCE_S <seconds>".
 //
 //   hxref_run --adam <n> <steps> <lr> <inv_record_steps> <beta1> <beta2> <eps> <impedance> <in.f64> <out.f64>
 // runs the reference's AdamOptimizer (src/optimizer/optimizer.cpp) on the CPU:
 // in.f64 holds n initial weights followed by steps x n gradients; out.f64
 // receives the weights after every step (steps x n) and the final m and v.
+#include <chrono>
 #include <cstdio>
 #include <cstdlib>
 #include <memory>
@@ -81,8 +90,8 @@ int main(int argc, char** argv) {
     const double dt = std::atof(argv[3]);
     const int nstep = std::atoi(argv[4]);
     const double v_init = std::atof(argv[5]);
-    if (ptype != 0) {
-        std::fprintf(stderr, "only permute type 0 is supported by this harness\n");
+    if (ptype != 0 && ptype != 1 && ptype != 3) {
+        std::fprintf(stderr, "permute type must be 0, 1 or 3\n");
         return 2;
     }
     std::vector<int> probes;
@@ -108,6 +117,10 @@ int main(int argc, char** argv) {
     // through the reference's gap API (pairs written by the exporter)
     {
         FILE* f = std::fopen((dir + "/halfgap.i32").c_str(), "rb");
+        if (f && ptype != 0) {
+            std::fprintf(stderr, "HalfGap wiring needs permute type 0\n");
+            return 2;
+        }
         if (f) {
             int pr[2];
             while (std::fread(pr, sizeof(int), 2, f) == 2) {
@@ -122,8 +135,11 @@ int main(int argc, char** argv) {
     }
     std::vector<VarDescriptor> monitors;
     sim->init_monitor_data_sets(monitors);
+    const auto t0 = std::chrono::steady_clock::now();
     sim->finitialize(v_init);
     HelioXroupData* g = sim->neuron_group_list[0];
+    if (g->permute)
+        for (int& q : probes) q = g->permute[q];
     std::vector<double> trace((size_t)(nstep + 1) * probes.size());
     auto record = [&](int row) {
         const double* v = g->vecdata_v->get_cpu_data();
@@ -134,6 +150,9 @@ int main(int argc, char** argv) {
         sim->fadvance();
         record(k + 1);
     }
+    const double secs = std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
+    std::printf("HXREF_FADVANCE_S %.9f\n", secs);
+    std::fflush(stdout);
     sim->output_spikes();
     FILE* f = std::fopen(argv[7], "wb");
     if (!f) return 3;

@@ -57,45 +57,146 @@ def _free_port():
     return p
 
 
-def _worker(rank, world, port, q):
+def _spawn(target, world=2, timeout=120):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=target, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = sorted([q.get(timeout=timeout) for _ in procs], key=lambda x: x[0])
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    return res
+
+
+def _init(rank, world, port):
     import datetime
 
-    import torch
     import torch.distributed as dist
 
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
+    return dist
+
+
+def _exchange_worker(rank, world, port, q):
+    import ctypes as C
+
+    dist = _init(rank, world, port)
     try:
+        fn = shard.allgather_exchange(device="cpu")
         cap = 5
         rng = np.random.default_rng(rank)
         n = 2 + rank
         gid = rng.integers(0, 100, n).astype(np.int32)
         step = rng.integers(0, 50, n).astype(np.int32)
-        buf = torch.from_numpy(shard.pad_spikes(gid, step, cap).reshape(-1))
-        out = [torch.zeros_like(buf) for _ in range(world)]
-        dist.all_gather(out, buf)
-        recv = torch.cat(out).numpy().reshape(-1, 2)
+        send = shard.pad_spikes(gid, step, cap)
+        recv = np.zeros((world * cap, 2), np.int32)
+        # the library's call: window buffer pointers, entries per rank, stream
+        fn(send.ctypes.data_as(C.c_void_p).value, recv.ctypes.data_as(C.c_void_p).value, cap, 0)
         q.put((rank, recv.tolist(), gid.tolist(), step.tolist()))
     finally:
         dist.destroy_process_group()
 
 
 def test_window_exchange_roundtrip_gloo():
-    ctx = mp.get_context("spawn")
-    q = ctx.Queue()
-    port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
-    for p in procs:
-        p.start()
-    res = [q.get(timeout=120) for _ in procs]
-    for p in procs:
-        p.join(timeout=60)
-        assert p.exitcode == 0
-    res.sort()
+    """The exchange hook all-gathers every rank's window buffer (host buffers over gloo)."""
+    res = _spawn(_exchange_worker)
     sent = {r: list(zip(g, s)) for r, _, g, s in res}
     for r, recv, _, _ in res:
         recv = np.asarray(recv)
         valid = [tuple(x) for x in recv if x[0] >= 0]
         assert valid == sent[0] + sent[1]
         assert recv.shape == (2 * 5, 2)
+
+
+# status bits of include/heliox_b200.h
+XS_LATE, XS_BUCKET, XS_WINDOW, XS_ABORT = 1, 2, 4, 8
+
+
+def _status_worker(rank, world, port, q):
+    """After the last window every rank all-gathers its (bits, bucket need)
+    pair and applies the library's merge rule.  Scenario 1 injects a host
+    failure on rank 1 (it reports HX_XS_ABORT, as the library does for a rank
+    that stopped launching work) while rank 0's buckets overflowed; scenario
+    2 has only bucket overflows of different sizes."""
+    import ctypes as C
+
+    dist = _init(rank, world, port)
+    try:
+        fn = shard.allgather_exchange(device="cpu")
+        out = []
+        for mine in ({0: (XS_BUCKET, 40), 1: (XS_ABORT, 0)}, {0: (XS_BUCKET, 40), 1: (XS_BUCKET, 90)}):
+            send = np.array(mine[rank], np.int32)
+            recv = np.zeros(2 * world, np.int32)
+            fn(send.ctypes.data_as(C.c_void_p).value, recv.ctypes.data_as(C.c_void_p).value, 1, 0)
+            out.append(shard.merge_status(recv))
+        q.put((rank, out))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_status_exchange_agrees_on_failure_gloo():
+    res = _spawn(_status_worker)
+    (_, a), (_, b) = res
+    assert a == b  # every rank reaches the same decision
+    assert a[0] == (XS_BUCKET | XS_ABORT, 40, 1)  # fail together, naming rank 1
+    assert a[1] == (XS_BUCKET, 90, 0)  # rerun together with the largest need
+
+
+def test_merge_status_rule():
+    assert shard.merge_status(np.array([[0, 3], [0, 7]])) == (0, 7, -1)
+    assert shard.merge_status(np.array([[XS_BUCKET, 3], [XS_WINDOW, 0], [XS_LATE, 1]])) == (7, 3, 1)
+
+
+def _allreduce_worker(rank, world, port, q):
+    """Data-parallel Adam: each rank's gradient (its own trial) summed by the
+    optimizer hook over gloo, then the reference's Adam update on every rank."""
+    import ctypes as C
+
+    from oracle import oracle as O
+
+    dist = _init(rank, world, port)
+    try:
+        fn = shard.allreduce_sum(device="cpu")
+        w0 = np.array([0.12, 0.036, 3e-4])
+        rng = np.random.default_rng(100 + rank)
+        grads = rng.standard_normal((3, 3))
+        summed = []
+        for g in grads:
+            buf = np.array(g, dtype=np.float64)  # a copy: the hook sums in place
+            fn(buf.ctypes.data_as(C.c_void_p).value, buf.shape[0], 0)
+            summed.append(buf.copy())
+        ws, _, _ = O.adam_port(w0, np.array(summed), 1e-3, 1.0)
+        q.put((rank, grads.tolist(), np.array(summed).tolist(), ws.tolist()))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_gradient_allreduce_before_adam_gloo():
+    res = _spawn(_allreduce_worker)
+    g0, g1 = np.array(res[0][1]), np.array(res[1][1])
+    for r in res:
+        assert np.array_equal(np.array(r[2]), g0 + g1)  # each rank holds the sum
+    assert np.array_equal(np.array(res[0][3]), np.array(res[1][3]))  # identical updates
+
+
+def test_config4_network_independent_of_rank_count():
+    """The strong-scaling network: its union over any number of ranks is the same network."""
+
+    def key(g):
+        cell = g.cell_of_node()
+        base = g.meta["gid_base"]
+        e = g.exp2syn
+        return sorted(zip((base + cell[e.nodes]).tolist(), e.ifields["src"].tolist(), e.fields["weight"].tolist(),
+                          e.fields["delay"].tolist(), g.meta["teacher_weight"].tolist()))
+
+    one = synth.network_config4_shard(9, 0, 1)
+    for n in (2, 3):
+        parts = [synth.network_config4_shard(9, r, n) for r in range(n)]
+        assert sum(p.nnode for p in parts) == one.nnode
+        assert sorted(sum((key(p) for p in parts), [])) == key(one)
+        assert [p.meta["gid_base"] for p in parts] == [synth.config4_cell_range(9, r, n)[0] for r in range(n)]
