@@ -135,7 +135,7 @@ struct hx_ctx {
     int window = 0, window_user = 0;
     double dmin = 0.0;
     hx::DevNet N{};
-    DevBuf<int> node_syn_off, pack_syn_off, syn_kind, src_off, src_syn;
+    DevBuf<int> node_syn_off, pack_syn_off, syn_kind, src_off, src_syn, syn_node, syn_pack;
     DevBuf<double> syn_tau1, syn_tau2, syn_cA, syn_cB, syn_fA, syn_fB, syn_delay;
     DevBuf<double> sA, sB, tA, tB, lA, lB;
     DevBuf<int> cs_ps_node, cs_gid, cs_ps_flag;

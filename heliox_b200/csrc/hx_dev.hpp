@@ -10,7 +10,11 @@ constexpr int kThreads = 512;  // threads per CTA (one CTA per cell pack, 16 war
 // registers (232 a thread) without spilling
 constexpr int kSplitThreads = 256;
 
-enum NodeFlag : int { kHasPas = 1, kHasHH = 2 };
+// kHasSyn: the node carries ExpSyn / Exp2Syn instances; kHasCpl: HalfGap,
+// gapjunction_lr or graded-synapse instances; kHasIn: it is the partner
+// (source / presynaptic node) of such an instance.  The per-node network
+// loops run only on flagged nodes.
+enum NodeFlag : int { kHasPas = 1, kHasHH = 2, kHasSyn = 4, kHasCpl = 8, kHasIn = 16 };
 
 // The execution plan and the model parameters.  Node arrays are in GPU
 // (pack-contiguous, cell-contiguous) order; density-mechanism parameters are
@@ -89,12 +93,17 @@ struct DevSplit {
 struct DevNet {
     // exponential synapses: B' = B + fB w, A' = A + fA w at an event;
     // x <- x + c (0 - x) per step (c = 1 - exp(-dt/tau)); i = (B - A)(v - e)
-    int nsyn, smem_syn;
+    // Synapse states, their adjoints and gradients live in global memory and
+    // are read and written only by the thread that owns the synapse's node
+    // (delivery, current, decay and the event weight gradients alike).
+    int nsyn, npack;
     const int *node_syn_off, *pack_syn_off;
+    const int* syn_node;  // GPU node of synapse j
     const double *syn_e, *syn_w, *syn_cA, *syn_cB, *syn_fA, *syn_fB;
-    double *sA, *sB;  // state between windows
+    double *sA, *sB;  // state
     double *tA, *tB;  // tape rows (k - k_base) x nsyn after the step's deliveries; null = no tape
-    // events: bucket k holds the synapses that receive an event at step k
+    // events: bucket (k, p) holds the synapses of pack p that receive an event
+    // at step k: ev_cnt[k * npack + p] entries from ev_syn[(k * npack + p) * ev_cap]
     const int *ev_cnt, *ev_syn;
     int ev_cap;
     // PreSyn threshold detection (one per cell slot; -1: none)

@@ -65,7 +65,7 @@ __global__ void lib_init_kernel(DevLib L, int nnode, double v_init) {
 // kLib adds the library mechanisms (hx_lib.cuh): their currents after the
 // other mechanisms in phase A, their state updates in phase C, and their
 // states in the tape (the cell's contiguous state range, row per step).
-template <bool kNet, bool kLib = false>
+template <bool kNet, bool kLib = false, bool kCpl = false>
 __global__ void __launch_bounds__(kThreads, 1) fwd_kernel(DevGroup G, DevState S, DevTape T, int write_tape,
                                                            DevProbe P, double* __restrict__ trace,
                                                            const double* __restrict__ tmid, int k0, int k1, DevNet N,
@@ -78,33 +78,28 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_kernel(DevGroup G, DevState S
     double* sd = srhs + N_;
     double* sa = sd + N_;
     double* sb = sa + N_;
-    double* scd = sb + N_;                        // per-branch contributions of hines_rt
+    double* scd = sb + N_;  // per-segment contributions and couplings of hines_rt
     double* scr = scd + G.smem_br;
-    double* ssA = scr + G.smem_br;                // kNet: synapse states of the pack
-    double* ssB = ssA + (kNet ? N.smem_syn : 0);
-    double* send = ssB + (kNet ? N.smem_syn : 0);
+    double* sfe = scr + G.smem_br;
+    double* sge = sfe + G.smem_br;
+    double* send = sge + G.smem_br;
     Meta M;
     Grp g;
     if (!setup_pack(G, p, reinterpret_cast<int*>(send), M, g)) return;
     const int pb = G.pack_node_off[p];
     const int i0 = g.nb, i1 = g.nb + g.n;
-    const bool rt = rt_fits(M, g);
     for (int i = i0 + g.tl; i < i1; i += g.nt) {
         sv[i] = S.v[pb + i];
         sa[i] = G.a[pb + i];
         sb[i] = G.b[pb + i];
     }
-    // kNet: the cell's synapses [c0, c1) (global ids), stored from ps0 in shared memory
-    int c0 = 0, c1 = 0, ps0 = 0, psnode = -1, psflag = 0, gid = 0;
+    // kNet: the cell's synapses [c0, c1) (global ids); their states N.sA/N.sB
+    // are touched only by the thread that owns the synapse's node
+    int c0 = 0, c1 = 0, psnode = -1, psflag = 0, gid = 0;
     double psthr = 0.0;
     if (kNet) {
-        ps0 = N.pack_syn_off[p];
         c0 = N.node_syn_off[pb + i0];
         c1 = N.node_syn_off[pb + i1];
-        for (int j = c0 + g.tl; j < c1; j += g.nt) {
-            ssA[j - ps0] = N.sA[j];
-            ssB[j - ps0] = N.sB[j];
-        }
         psnode = N.cs_ps_node[g.slot];
         if (psnode >= 0) {
             psflag = N.cs_ps_flag[g.slot];
@@ -118,6 +113,9 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_kernel(DevGroup G, DevState S
         ls0 = L.ent_st[L.node_off[pb + i0]];
         ls1 = L.ent_st[L.node_off[pb + i1]];
     }
+    // kNet: the event count of the next step's bucket, read one step ahead
+    // (all buckets of the launch's steps are routed before the launch)
+    int ev_next = (kNet && k0 < k1) ? N.ev_cnt[(size_t)k0 * N.npack + p] : 0;
     g.sync();
     if (k0 == 0 && trace)
         for (int q = q0 + g.tl; q < q1; q += g.nt) trace[P.slot[q]] = sv[P.local[q]];
@@ -142,22 +140,17 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_kernel(DevGroup G, DevState S
                     psflag = 0;
                 }
             }
-            const int cnt = min(N.ev_cnt[k], N.ev_cap);
-            const int* ev = N.ev_syn + (size_t)k * N.ev_cap;
-            for (int e = g.tl; e < cnt; e += g.nt) {
+            // the step's events of this pack: the owner of the synapse's node adds them
+            const size_t b = (size_t)k * N.npack + p;
+            const int cnt = min(ev_next, N.ev_cap);
+            if (k + 1 < k1) ev_next = N.ev_cnt[b + N.npack];
+            const int* ev = N.ev_syn + b * N.ev_cap;
+            for (int e = 0; e < cnt; ++e) {
                 const int j = ev[e];
-                if (j >= c0 && j < c1) {
+                if (j >= c0 && j < c1 && (__ldg(N.syn_node + j) - pb - i0) % g.nt == g.tl) {
                     const double w = __ldg(N.syn_w + j);
-                    atomicAdd(ssA + (j - ps0), w * __ldg(N.syn_fA + j));
-                    atomicAdd(ssB + (j - ps0), w * __ldg(N.syn_fB + j));
-                }
-            }
-            g.sync();
-            if (N.tA) {
-                const size_t off = (size_t)(k - T.k_base) * (size_t)N.nsyn;
-                for (int j = c0 + g.tl; j < c1; j += g.nt) {
-                    N.tA[off + j] = ssA[j - ps0];
-                    N.tB[off + j] = ssB[j - ps0];
+                    N.sA[j] += w * __ldg(N.syn_fA + j);
+                    N.sB[j] += w * __ldg(N.syn_fB + j);
                 }
             }
         }
@@ -166,10 +159,17 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_kernel(DevGroup G, DevState S
         // their cnexp update from v_k is applied here, one step late, so that
         // they are read once per step together with the parameters (at the
         // launch's first step S holds the current gates already).
+        SynNext nx;
+        if (kNet) syn_next(G, N, M, pb, i0 + g.tl, i1, nx);
         for (int i = i0 + g.tl; i < i1; i += g.nt) {
             const int fl = M.flag[i];
             NodePar q;
             load_par(G, pb + i, fl, q);
+            SynPre sp;
+            if (kNet) {
+                load_syn(N, nx, N.sA, N.sB, sp);
+                syn_next(G, N, M, pb, i + g.nt, i1, nx);
+            }
             double gm = 0.0, gh = 0.0, gn = 0.0;
             if (fl & kHasHH) {
                 gm = S.m[pb + i];
@@ -195,7 +195,7 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_kernel(DevGroup G, DevState S
             double r, dd;
             if (kNet) {
                 const int gi = pb + i;
-                if (N.coupled) {  // graded synapses: s_k from s_{k-1} and vpre_k (deferred cnexp update)
+                if (kCpl && (fl & kHasCpl)) {  // graded synapses: s_k from s_{k-1} and vpre_k (deferred cnexp update)
                     const int r1 = __ldg(N.node_gr_off + gi + 1);
                     for (int j = __ldg(N.node_gr_off + gi); j < r1; ++j) {
                         double sj = N.gr_s[j];
@@ -210,12 +210,12 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_kernel(DevGroup G, DevState S
                         if (write_tape) N.tS[(size_t)(k - T.k_base + 1) * N.ngr + j] = sj;
                     }
                 }
-                assemble<true, true>(G, M, pb, i, fl, q, vi, sv, sa, sb, gm, gh, gn, tm, r, dd, N, ssA, ssB, ps0,
-                                     N.gr_s, N.vpeer);
+                assemble<true, true, false, false, kCpl>(G, M, pb, i, fl, q, vi, sv, sa, sb, gm, gh, gn, tm, r, dd, N,
+                                                         N.sA, N.sB, sp, N.gr_s, N.vpeer);
             } else if (kLib) {
                 double ica;
                 assemble<true, false, false, true>(G, M, pb, i, fl, q, vi, sv, sa, sb, gm, gh, gn, tm, r, dd, N,
-                                                   nullptr, nullptr, 0, nullptr, nullptr, &L, L.st, &ica);
+                                                   nullptr, nullptr, SynPre{}, nullptr, nullptr, &L, L.st, &ica);
                 L.nica[pb + i] = ica;
             } else {
                 assemble<true>(G, M, pb, i, fl, q, vi, sv, sa, sb, gm, gh, gn, tm, r, dd);
@@ -225,20 +225,24 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_kernel(DevGroup G, DevState S
         }
         g.sync();
         // B: Hines solve (rhs := dv)
-        if (rt)
-            hines_rt<false>(M, g, sa, sb, sd, srhs, scd, scr);
-        else
-            hines_cell<false>(M, g, sa, sb, sd, srhs);
+        hines_rt<false>(M, g, sa, sb, sd, srhs, scd, scr, sfe, sge);
         // C: v update (the gates follow in the next step's A, or below)
-        for (int i = i0 + g.tl; i < i1; i += g.nt) {
-            sv[i] = sv[i] + srhs[i];
-            if (kNet) {  // synapse decay x + c (0 - x) (expsyn.cpp:125-134, exp2syn_temp.cuh:51-58)
-                const int s1 = __ldg(N.node_syn_off + pb + i + 1);
-                for (int j = __ldg(N.node_syn_off + pb + i); j < s1; ++j) {
-                    const double A = ssA[j - ps0], B = ssB[j - ps0];
-                    ssA[j - ps0] = A + __ldg(N.syn_cA + j) * (0.0 - A);
-                    ssB[j - ps0] = B + __ldg(N.syn_cB + j) * (0.0 - B);
+        for (int i = i0 + g.tl; i < i1; i += g.nt) sv[i] = sv[i] + srhs[i];
+        if (kNet) {
+            // the cell's synapses, coalesced over its threads (every owner's
+            // reads of phase A are behind the barrier above; the next step's
+            // deliveries behind the one below): states after this step's
+            // deliveries into the tape, then the decay x + c (0 - x)
+            // (expsyn.cpp:125-134, exp2syn_temp.cuh:51-58)
+            const size_t toffs = (size_t)(k - T.k_base) * (size_t)N.nsyn;
+            for (int j = c0 + g.tl; j < c1; j += g.nt) {
+                const double A = N.sA[j], B = N.sB[j];
+                if (N.tA) {
+                    N.tA[toffs + j] = A;
+                    N.tB[toffs + j] = B;
                 }
+                N.sA[j] = A + __ldg(N.syn_cA + j) * (0.0 - A);
+                N.sB[j] = B + __ldg(N.syn_cB + j) * (0.0 - B);
             }
         }
         // library states at the new v, type by type over this thread's nodes
@@ -255,7 +259,7 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_kernel(DevGroup G, DevState S
             for (int j = ls0 + g.tl; j < ls1; j += g.nt) __stcs(row + j, L.st[j]);
         }
     }
-    double* vdst = (kNet && N.coupled) ? N.vout : S.v;
+    double* vdst = kCpl ? N.vout : S.v;
     for (int i = i0 + g.tl; i < i1; i += g.nt) {
         vdst[pb + i] = sv[i];
         if ((M.flag[i] & kHasHH) && k1 > k0) {  // gates of step k1 (the update the last step deferred)
@@ -267,13 +271,7 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_kernel(DevGroup G, DevState S
             S.n[pb + i] = gate_step(gn, rt.inf[2], rt.k[2], G.dt);
         }
     }
-    if (kNet) {
-        for (int j = c0 + g.tl; j < c1; j += g.nt) {
-            N.sA[j] = ssA[j - ps0];
-            N.sB[j] = ssB[j - ps0];
-        }
-        if (g.tl == 0 && psnode >= 0) N.cs_ps_flag[g.slot] = psflag;
-    }
+    if (kNet && g.tl == 0 && psnode >= 0) N.cs_ps_flag[g.slot] = psflag;
 }
 
 // ------------------------------------------------------------------ backward
@@ -294,7 +292,7 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_kernel(DevGroup G, DevState S
 // kLib: the library mechanisms' state-update adjoints join mu in S + A (their
 // currents recomputed from the tape give d_k and the calcium current), the
 // adjoints of their currents join dL/dv_k in V (hx_lib.cuh).
-template <bool kNet, bool kLib = false>
+template <bool kNet, bool kLib = false, bool kCpl = false>
 __global__ void __launch_bounds__(kThreads, 1) bwd_kernel(DevGroup G, DevTape T, DevAdj Ad, DevGrad GR, DevProbe P,
                                                            const double* __restrict__ dLdv,
                                                            const double* __restrict__ tmid, int k_hi, int k_lo,
@@ -309,17 +307,16 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_kernel(DevGroup G, DevTape T,
     double* sd = sw + N_;
     double* sa = sd + N_;
     double* sb = sa + N_;
-    double* scd = sb + N_;  // per-branch contributions of hines_rt
+    double* scd = sb + N_;  // per-segment contributions and couplings of hines_rt
     double* scr = scd + G.smem_br;
-    double* slA = scr + G.smem_br;  // kNet: synapse adjoints of the pack
-    double* slB = slA + (kNet ? N.smem_syn : 0);
-    double* send = slB + (kNet ? N.smem_syn : 0);
+    double* sfe = scr + G.smem_br;
+    double* sge = sfe + G.smem_br;
+    double* send = sge + G.smem_br;
     Meta M;
     Grp g;
     if (!setup_pack(G, p, reinterpret_cast<int*>(send), M, g)) return;
     const int pb = G.pack_node_off[p];
     const int i0 = g.nb, i1 = g.nb + g.n;
-    const bool rt = rt_fits(M, g);
     const double dt = G.dt, q10 = G.q10;
     double* __restrict__ lv = Ad.lv + pb;
     double* __restrict__ lmv = Ad.lm + pb;
@@ -328,7 +325,7 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_kernel(DevGroup G, DevTape T,
     for (int i = i0 + g.tl; i < i1; i += g.nt) {
         sa[i] = G.a[pb + i];
         sb[i] = G.b[pb + i];
-        if (kNet && N.coupled) {  // partner contributions to dL/dv_{k_hi} from the launch of step k_hi
+        if (kCpl && (M.flag[i] & kHasIn)) {  // partner contributions to dL/dv_{k_hi} from the launch of step k_hi
             double l = lv[i];
             const int e1 = __ldg(N.node_in_off + pb + i + 1);
             for (int e = __ldg(N.node_in_off + pb + i); e < e1; ++e) {
@@ -338,15 +335,14 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_kernel(DevGroup G, DevTape T,
             lv[i] = l;
         }
     }
-    int c0 = 0, c1 = 0, ps0 = 0;
+    // kNet: the cell's synapses [c0, c1); their adjoints Ad.lA/Ad.lB and
+    // gradients are touched only by the thread that owns the synapse's node
+    int c0 = 0, c1 = 0;
+    double* __restrict__ slA = Ad.lA;
+    double* __restrict__ slB = Ad.lB;
     if (kNet) {
-        ps0 = N.pack_syn_off[p];
         c0 = N.node_syn_off[pb + i0];
         c1 = N.node_syn_off[pb + i1];
-        for (int j = c0 + g.tl; j < c1; j += g.nt) {
-            slA[j - ps0] = Ad.lA[j];
-            slB[j - ps0] = Ad.lB[j];
-        }
     }
     const int q0 = P.slot_off[g.slot], q1 = P.slot_off[g.slot + 1];
     g.sync();
@@ -357,9 +353,17 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_kernel(DevGroup G, DevTape T,
         const double tm = tmid[k];
         const double* tA = kNet ? N.tA + (size_t)(k - T.k_base) * (size_t)N.nsyn : nullptr;
         const double* tB = kNet ? N.tB + (size_t)(k - T.k_base) * (size_t)N.nsyn : nullptr;
-        const double* grs = (kNet && N.coupled) ? N.tS + (size_t)(k - T.k_base + 1) * N.ngr : nullptr;
+        const double* grs = kCpl ? N.tS + (size_t)(k - T.k_base + 1) * N.ngr : nullptr;
+        const int ev_k = kNet ? N.ev_cnt[(size_t)k * N.npack + p] : 0;  // used at the step's end
         const double* vpeer = T.v + (size_t)(k - T.k_base) * (size_t)G.nnode;
         // S + A
+        if (kNet)  // synapse-state adjoints through the decay (the cell's synapses, coalesced)
+            for (int j = c0 + g.tl; j < c1; j += g.nt) {
+                slA[j] *= 1.0 - __ldg(N.syn_cA + j);
+                slB[j] *= 1.0 - __ldg(N.syn_cB + j);
+            }
+        SynNext nx;
+        if (kNet) syn_next(G, N, M, pb, i0 + g.tl, i1, nx);
         for (int i = i0 + g.tl; i < i1; i += g.nt) {
             const int fl = M.flag[i];
             double mu = lv[i];
@@ -380,18 +384,16 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_kernel(DevGroup G, DevTape T,
             load_par(G, pb + i, fl, q);
             double r, dd;
             if (kNet) {
-                const int s1 = __ldg(N.node_syn_off + pb + i + 1);
-                for (int j = __ldg(N.node_syn_off + pb + i); j < s1; ++j) {
-                    slA[j - ps0] *= 1.0 - __ldg(N.syn_cA + j);
-                    slB[j - ps0] *= 1.0 - __ldg(N.syn_cB + j);
-                }
-                assemble<false, true>(G, M, pb, i, fl, q, vk, nullptr, sa, sb, gm, gh, gn, tm, r, dd, N, tA, tB, 0,
-                                      grs, vpeer);
+                SynPre sp;
+                load_syn(N, nx, tA, tB, sp);
+                syn_next(G, N, M, pb, i + g.nt, i1, nx);
+                assemble<false, true, false, false, kCpl>(G, M, pb, i, fl, q, vk, nullptr, sa, sb, gm, gh, gn, tm, r,
+                                                          dd, N, tA, tB, sp, grs, vpeer);
             } else if (kLib) {
                 const double* Xk = L.tape + (size_t)(k - L.k_base) * (size_t)L.nst;
                 double ica;
                 assemble<false, false, false, true>(G, M, pb, i, fl, q, vk, nullptr, sa, sb, gm, gh, gn, tm, r, dd,
-                                                    N, nullptr, nullptr, 0, nullptr, nullptr, &L, Xk, &ica);
+                                                    N, nullptr, nullptr, SynPre{}, nullptr, nullptr, &L, Xk, &ica);
                 mu += lib::lib_state_adj(L, pb + i, T.v[off + G.nnode + i], Xk, Xk + L.nst, ica);
             } else {
                 assemble<false>(G, M, pb, i, fl, q, vk, nullptr, sa, sb, gm, gh, gn, tm, r, dd);
@@ -402,20 +404,31 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_kernel(DevGroup G, DevTape T,
         }
         g.sync();
         // B: w = M^{-T} mu
-        if (rt)
-            hines_rt<true>(M, g, sa, sb, sd, sw, scd, scr);
-        else
-            hines_cell<true>(M, g, sa, sb, sd, sw);
+        hines_rt<true>(M, g, sa, sb, sd, sw, scd, scr, sfe, sge);
         if (k > k_lo && g.tl < 4) {  // the next step's tape rows of the cell, into L2 (read after this phase)
             const double* row = (g.tl == 0 ? T.v : g.tl == 1 ? T.m : g.tl == 2 ? T.h : T.n) + off - G.nnode + i0;
             prefetch_l2(row, sizeof(double) * (size_t)(i1 - i0));
         }
         // V
+        if (kNet) syn_next(G, N, M, pb, i0 + g.tl, i1, nx);
         for (int i = i0 + g.tl; i < i1; i += g.nt) {
             const int gi = pb + i;
             const int fl = M.flag[i];
             NodePar q;
             load_par(G, gi, fl, q);
+            // the node's first synapse: tape states and reversal potential, and
+            // its adjoints and e-gradient (read-modify-written below)
+            SynPre sp;
+            double la0 = 0.0, lb0 = 0.0, ge0 = 0.0;
+            if (kNet) {
+                load_syn(N, nx, tA, tB, sp);
+                syn_next(G, N, M, pb, i + g.nt, i1, nx);
+                if (sp.s0 < sp.s1) {
+                    la0 = slA[sp.s0];
+                    lb0 = slB[sp.s0];
+                    ge0 = GR.syn_e[sp.s0];
+                }
+            }
             const double w = sw[i];
             const double vk = T.v[off + i];
             // last read of row k+1 (streaming load); rows are read twice, once as
@@ -435,18 +448,24 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_kernel(DevGroup G, DevTape T,
                 lhv[i] = lh;
                 lnv[i] = ln;
             }
-            if (kNet) {
-                const double sarea = 1.e2 / __ldg(G.area + gi);
-                const int s1 = __ldg(N.node_syn_off + gi + 1);
-                for (int j = __ldg(N.node_syn_off + gi); j < s1; ++j) {
-                    const double Gs = tB[j] - tA[j], e = __ldg(N.syn_e + j);
-                    const double lG = sarea * (ld - w * (vk - e));
-                    slB[j - ps0] += lG;
-                    slA[j - ps0] -= lG;
-                    GR.syn_e[j] += w * sarea * Gs;
+            if (kNet && (fl & (kHasSyn | kHasCpl))) {
+                const double sarea = sp.sarea;
+                if (fl & kHasSyn) {
+                    double Gs = sp.B0 - sp.A0, lG = sarea * (ld - w * (vk - sp.E0));
+                    slB[sp.s0] = lb0 + lG;
+                    slA[sp.s0] = la0 - lG;
+                    GR.syn_e[sp.s0] = ge0 + w * sarea * Gs;
                     lvn -= w * sarea * Gs;
+                    for (int j = sp.s0 + 1; j < sp.s1; ++j) {
+                        Gs = tB[j] - tA[j];
+                        lG = sarea * (ld - w * (vk - __ldg(N.syn_e + j)));
+                        slB[j] += lG;
+                        slA[j] -= lG;
+                        GR.syn_e[j] += w * sarea * Gs;
+                        lvn -= w * sarea * Gs;
+                    }
                 }
-                if (N.coupled) {
+                if (kCpl && (fl & kHasCpl)) {
                     const int h1 = __ldg(N.node_hg_off + gi + 1);
                     for (int j = __ldg(N.node_hg_off + gi); j < h1; ++j) {
                         const int src = __ldg(N.hg_src + j);
@@ -501,23 +520,18 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_kernel(DevGroup G, DevTape T,
             }
             lv[i] = lvn;
         }
-        if (kNet) {  // event weight gradients: dL/dw += fA lA' + fB lB' per delivery at step k
-            g.sync();
-            const int cnt = min(N.ev_cnt[k], N.ev_cap);
-            const int* ev = N.ev_syn + (size_t)k * N.ev_cap;
-            for (int e = g.tl; e < cnt; e += g.nt) {
+        if (kNet) {  // event weight gradients: dL/dw += fA lA' + fB lB' per delivery at step k (owner thread)
+            const size_t b = (size_t)k * N.npack + p;
+            const int cnt = min(ev_k, N.ev_cap);
+            const int* ev = N.ev_syn + b * N.ev_cap;
+            for (int e = 0; e < cnt; ++e) {
                 const int j = ev[e];
-                if (j >= c0 && j < c1)
-                    atomicAdd(GR.syn_w + j, __ldg(N.syn_fA + j) * slA[j - ps0] + __ldg(N.syn_fB + j) * slB[j - ps0]);
+                if (j >= c0 && j < c1 && (__ldg(N.syn_node + j) - pb - i0) % g.nt == g.tl)
+                    GR.syn_w[j] += __ldg(N.syn_fA + j) * slA[j] + __ldg(N.syn_fB + j) * slB[j];
             }
         }
         g.sync();
     }
-    if (kNet)
-        for (int j = c0 + g.tl; j < c1; j += g.nt) {
-            Ad.lA[j] = slA[j - ps0];
-            Ad.lB[j] = slB[j - ps0];
-        }
 }
 
 // ------------------------------------------------------------------ small kernels
@@ -647,11 +661,11 @@ cudaError_t launch_f32_to_f64(const float* a, double* b, int n, cudaStream_t st)
 }
 
 // ------------------------------------------------------------------ launchers
-size_t fwd_smem_bytes(const DevGroup& G, int smem_syn) {
-    return sizeof(double) * (5 * (size_t)G.smem_n + 2 * (size_t)G.smem_br + 2 * (size_t)smem_syn) + meta_bytes(G);
+size_t fwd_smem_bytes(const DevGroup& G) {
+    return sizeof(double) * (5 * (size_t)G.smem_n + 4 * (size_t)G.smem_br) + meta_bytes(G);
 }
-size_t bwd_smem_bytes(const DevGroup& G, int smem_syn) {
-    return sizeof(double) * (4 * (size_t)G.smem_n + 2 * (size_t)G.smem_br + 2 * (size_t)smem_syn) + meta_bytes(G);
+size_t bwd_smem_bytes(const DevGroup& G) {
+    return sizeof(double) * (4 * (size_t)G.smem_n + 4 * (size_t)G.smem_br) + meta_bytes(G);
 }
 // split-cell kernels (hx_split.cu) keep the gates / node adjoints in shared memory
 size_t split_fwd_smem_bytes(const DevGroup& G) { return sizeof(double) * 8 * (size_t)G.smem_n + meta_bytes(G); }
@@ -667,6 +681,12 @@ cudaError_t configure_kernels(size_t smem_fwd, size_t smem_bwd, size_t smem_fwd_
     e = cudaFuncSetAttribute(bwd_kernel<false, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_bwd);
     if (e != cudaSuccess) return e;
     e = cudaFuncSetAttribute(fwd_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_fwd_net);
+    if (e != cudaSuccess) return e;
+    e = cudaFuncSetAttribute(fwd_kernel<true, false, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)smem_fwd_net);
+    if (e != cudaSuccess) return e;
+    e = cudaFuncSetAttribute(bwd_kernel<true, false, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)smem_bwd_net);
     if (e != cudaSuccess) return e;
     return cudaFuncSetAttribute(bwd_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_bwd_net);
 }
@@ -686,15 +706,19 @@ cudaError_t launch_fwd(const DevGroup& G, const DevState& S, const DevTape& T, i
                        double* trace, const double* tmid, int k0, int k1, cudaStream_t st, const DevNet* N,
                        const DevLib* L) {
     if (N) {
-        fwd_kernel<true><<<G.npack, kThreads, fwd_smem_bytes(G, N->smem_syn), st>>>(G, S, T, write_tape, P, trace,
+        if (N->coupled)
+            fwd_kernel<true, false, true><<<G.npack, kThreads, fwd_smem_bytes(G), st>>>(G, S, T, write_tape, P, trace,
+                                                                                   tmid, k0, k1, *N, DevLib{});
+        else
+            fwd_kernel<true><<<G.npack, kThreads, fwd_smem_bytes(G), st>>>(G, S, T, write_tape, P, trace,
                                                                                    tmid, k0, k1, *N, DevLib{});
     } else if (L) {
         DevLib Lk = *L;
         Lk.k_base = T.k_base;
-        fwd_kernel<false, true><<<G.npack, kThreads, fwd_smem_bytes(G, 0), st>>>(G, S, T, write_tape, P, trace,
+        fwd_kernel<false, true><<<G.npack, kThreads, fwd_smem_bytes(G), st>>>(G, S, T, write_tape, P, trace,
                                                                                 tmid, k0, k1, DevNet{}, Lk);
     } else {
-        fwd_kernel<false><<<G.npack, kThreads, fwd_smem_bytes(G, 0), st>>>(G, S, T, write_tape, P, trace, tmid, k0,
+        fwd_kernel<false><<<G.npack, kThreads, fwd_smem_bytes(G), st>>>(G, S, T, write_tape, P, trace, tmid, k0,
                                                                           k1, DevNet{}, DevLib{});
     }
     return cudaGetLastError();
@@ -704,15 +728,19 @@ cudaError_t launch_bwd(const DevGroup& G, const DevTape& T, const DevAdj& A, con
                        const double* dLdv, const double* tmid, int k_hi, int k_lo, cudaStream_t st, const DevNet* N,
                        const DevLib* L) {
     if (N) {
-        bwd_kernel<true><<<G.npack, kThreads, bwd_smem_bytes(G, N->smem_syn), st>>>(G, T, A, GR, P, dLdv, tmid, k_hi,
+        if (N->coupled)
+            bwd_kernel<true, false, true><<<G.npack, kThreads, bwd_smem_bytes(G), st>>>(G, T, A, GR, P, dLdv, tmid, k_hi,
+                                                                                   k_lo, *N, DevLib{});
+        else
+            bwd_kernel<true><<<G.npack, kThreads, bwd_smem_bytes(G), st>>>(G, T, A, GR, P, dLdv, tmid, k_hi,
                                                                                    k_lo, *N, DevLib{});
     } else if (L) {
         DevLib Lk = *L;
         Lk.k_base = T.k_base;
-        bwd_kernel<false, true><<<G.npack, kThreads, bwd_smem_bytes(G, 0), st>>>(G, T, A, GR, P, dLdv, tmid, k_hi,
+        bwd_kernel<false, true><<<G.npack, kThreads, bwd_smem_bytes(G), st>>>(G, T, A, GR, P, dLdv, tmid, k_hi,
                                                                                 k_lo, DevNet{}, Lk);
     } else {
-        bwd_kernel<false><<<G.npack, kThreads, bwd_smem_bytes(G, 0), st>>>(G, T, A, GR, P, dLdv, tmid, k_hi, k_lo,
+        bwd_kernel<false><<<G.npack, kThreads, bwd_smem_bytes(G), st>>>(G, T, A, GR, P, dLdv, tmid, k_hi, k_lo,
                                                                           DevNet{}, DevLib{});
     }
     return cudaGetLastError();
@@ -772,13 +800,16 @@ __global__ void init_net_kernel(int nsyn, double* sA, double* sB, int ngr, const
 // Event routing: every spike (source gid, step j) reaches the local synapses
 // of its source; the delivery step is the first k >= j with
 // t_j + delay <= t_k + dt/2 (the reference's post_spike_receive condition,
-// postsyn.cpp:43-61, applied at the start of every step).  Events before
-// k_min (inside an already simulated window) set bit 1 of *err, a full bucket
-// bit 2; bucket counts keep counting past ev_cap so the needed size is known.
+// postsyn.cpp:43-61, applied at the start of every step).  The event goes to
+// the bucket of (step, the synapse's pack), so a CTA reads only its own
+// events.  Events before k_min (inside an already simulated window) set bit 1
+// of *err, a full bucket bit 2; bucket counts keep counting past ev_cap so
+// the needed size is known.
 __global__ void route_kernel(const int2* __restrict__ spk, const int* __restrict__ nspk_dev, int nspk_max,
                              const int* __restrict__ src_off, const int* __restrict__ src_syn, int nsrc,
                              const double* __restrict__ delay, const double* __restrict__ tstart, int nstep,
-                             double half_dt, int k_min, int* ev_cnt, int* ev_syn, int ev_cap, int* err) {
+                             double half_dt, int k_min, const int* __restrict__ syn_pack, int npack, int* ev_cnt,
+                             int* ev_syn, int ev_cap, int* err) {
     const int n = nspk_dev ? min(*nspk_dev, nspk_max) : nspk_max;
     for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
         const int2 sp = spk[i];
@@ -801,9 +832,10 @@ __global__ void route_kernel(const int2* __restrict__ spk, const int* __restrict
                 atomicOr(err, 1);
                 continue;
             }
-            const int c = atomicAdd(ev_cnt + lo, 1);
+            const size_t b = (size_t)lo * npack + __ldg(syn_pack + syn);
+            const int c = atomicAdd(ev_cnt + b, 1);
             if (c < ev_cap)
-                ev_syn[(size_t)lo * ev_cap + c] = syn;
+                ev_syn[b * ev_cap + c] = syn;
             else
                 atomicOr(err, 2);
         }
@@ -864,12 +896,13 @@ cudaError_t launch_init_net(int nsyn, double* sA, double* sB, int ngr, const dou
 
 cudaError_t launch_route(const int2* spk, const int* nspk_dev, int nspk_max, const int* src_off, const int* src_syn,
                          int nsrc, const double* delay, const double* tstart, int nstep, double half_dt, int k_min,
-                         int* ev_cnt, int* ev_syn, int ev_cap, int* err, cudaStream_t st) {
+                         const int* syn_pack, int npack, int* ev_cnt, int* ev_syn, int ev_cap, int* err,
+                         cudaStream_t st) {
     if (nspk_max <= 0) return cudaSuccess;
     int blocks = (nspk_max + 255) / 256;
     if (blocks > 4 * 148) blocks = 4 * 148;
     route_kernel<<<blocks, 256, 0, st>>>(spk, nspk_dev, nspk_max, src_off, src_syn, nsrc, delay, tstart, nstep,
-                                         half_dt, k_min, ev_cnt, ev_syn, ev_cap, err);
+                                         half_dt, k_min, syn_pack, npack, ev_cnt, ev_syn, ev_cap, err);
     return cudaGetLastError();
 }
 

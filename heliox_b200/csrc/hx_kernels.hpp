@@ -7,8 +7,8 @@
 
 namespace hx {
 
-size_t fwd_smem_bytes(const DevGroup& G, int smem_syn = 0);
-size_t bwd_smem_bytes(const DevGroup& G, int smem_syn = 0);
+size_t fwd_smem_bytes(const DevGroup& G);
+size_t bwd_smem_bytes(const DevGroup& G);
 size_t split_fwd_smem_bytes(const DevGroup& G);
 size_t split_bwd_smem_bytes(const DevGroup& G);
 cudaError_t configure_kernels(size_t smem_fwd, size_t smem_bwd, size_t smem_fwd_net, size_t smem_bwd_net);
@@ -38,7 +38,8 @@ cudaError_t launch_init_net(int nsyn, double* sA, double* sB, int ngr, const dou
                             double v_init, cudaStream_t st);
 cudaError_t launch_route(const int2* spk, const int* nspk_dev, int nspk_max, const int* src_off, const int* src_syn,
                          int nsrc, const double* delay, const double* tstart, int nstep, double half_dt, int k_min,
-                         int* ev_cnt, int* ev_syn, int ev_cap, int* err, cudaStream_t st);
+                         const int* syn_pack, int npack, int* ev_cnt, int* ev_syn, int ev_cap, int* err,
+                         cudaStream_t st);
 cudaError_t launch_log_append(const int2* win, const int* win_n, int win_cap, int2* log, int* log_n, int log_cap,
                               int* err, cudaStream_t st);
 cudaError_t launch_net_status(const int* err, const int* ev_cnt, int nstep, int extra, int2* out, cudaStream_t st);

@@ -278,36 +278,88 @@ std::string build_plan(const hx_group_desc& g, int nodes_per_warp, int max_pack_
         long long total = 0;
         for (int c : order) total += usize[c];
         const int avail = std::max(1, nsm - b0);
-        // waves: enough CTA capacity with a few percent left for fragmentation
-        const long long per_wave = (long long)avail * (long long)(cap * 0.96);
-        int waves = (int)std::max<long long>(1, (total + per_wave - 1) / std::max<long long>(per_wave, 1));
-        long long K = (long long)avail * waves;
-        K = std::max<long long>(K, ((long long)order.size() + kW - 1) / kW);
-        K = std::min<long long>(K, (long long)order.size());
-        std::set<std::pair<long long, int>> load;  // (nodes, bin)
-        for (long long k = 0; k < K; k++) {
-            bins.push_back({});
-            bin_n.push_back(0);
-            load.insert({0, (int)(b0 + k)});
-        }
-        for (int c : order) {
-            int b = -1;
-            for (auto it = load.begin(); it != load.end(); ++it) {
-                const int k = it->second;
-                if ((int)bins[k].size() < kW && bin_n[k] + usize[c] <= cap) {
-                    b = k;
-                    load.erase(it);
-                    break;
-                }
-            }
-            if (b < 0) {
+        // Waves: the step kernels are latency bound, so a wave of CTAs takes
+        // about the same time whatever their fill; the fewest waves that hold
+        // the cells win.  Start from the capacity bound and, for each wave
+        // count, deal the cells largest first to the least loaded CTA (LPT,
+        // balanced); at high fill LPT can leave every CTA with less room than
+        // the remaining cells, so those are then packed best-fit decreasing
+        // (the fullest CTA that still holds the cell) into the same CTAs.
+        // Only when both leave a cell over does the plan take one more wave.
+        // Two capacities: a soft one (91 % of the shared-memory bound, 4 % left
+        // for fragmentation) under which LPT and the balancing below have
+        // room to even out the CTAs' step times, and the hard bound itself,
+        // used (with best-fit packing) only when it saves a wave.
+        const long long per_wave_max = (long long)avail * (long long)cap;
+        const int waves_min =
+            (int)std::max<long long>(1, (total + per_wave_max - 1) / std::max<long long>(per_wave_max, 1));
+        const int soft = std::max(maxcell, (int)(0.91 * cap));
+        const long long per_wave_soft = (long long)avail * (long long)(0.96 * soft);
+        const int waves_soft =
+            (int)std::max<long long>(1, (total + per_wave_soft - 1) / std::max<long long>(per_wave_soft, 1));
+        int waves = waves_min;
+        if (waves_soft == waves_min) cap = soft;
+        const size_t nbase = bins.size();
+        for (;; waves++) {
+            long long K = (long long)avail * waves;
+            K = std::max<long long>(K, ((long long)order.size() + kW - 1) / kW);
+            K = std::min<long long>(K, (long long)order.size());
+            bins.resize(nbase);
+            bin_n.resize(nbase);
+            for (long long k = 0; k < K; k++) {
                 bins.push_back({});
                 bin_n.push_back(0);
-                b = (int)bins.size() - 1;
             }
-            bins[b].push_back(c);
-            bin_n[b] += usize[c];
-            if ((int)bins[b].size() < kW) load.insert({bin_n[b], b});
+            auto fits = [&](int k, int c) { return (int)bins[k].size() < kW && bin_n[k] + usize[c] <= cap; };
+            // LPT
+            std::set<std::pair<long long, int>> load;  // (nodes, bin)
+            for (long long k = 0; k < K; k++) load.insert({0, (int)(b0 + k)});
+            std::vector<int> left;
+            for (int c : order) {
+                int b = -1;
+                for (auto it = load.begin(); it != load.end(); ++it)
+                    if (fits(it->second, c)) {
+                        b = it->second;
+                        load.erase(it);
+                        break;
+                    }
+                if (b < 0) {
+                    left.push_back(c);
+                    continue;
+                }
+                bins[b].push_back(c);
+                bin_n[b] += usize[c];
+                if ((int)bins[b].size() < kW) load.insert({bin_n[b], b});
+            }
+            if (left.empty()) break;
+            // best-fit decreasing from scratch into the same CTAs
+            for (size_t k = nbase; k < bins.size(); k++) {
+                bins[k].clear();
+                bin_n[k] = 0;
+            }
+            left.clear();
+            std::multiset<std::pair<long long, int>> room;  // (free nodes, bin)
+            for (size_t k = nbase; k < bins.size(); k++) room.insert({(long long)cap, (int)k});
+            for (int c : order) {
+                auto it = room.lower_bound({(long long)usize[c], -1});
+                if (it == room.end()) {
+                    left.push_back(c);
+                    continue;
+                }
+                const int b = it->second;
+                room.erase(it);
+                bins[b].push_back(c);
+                bin_n[b] += usize[c];
+                if ((int)bins[b].size() < kW) room.insert({(long long)cap - bin_n[b], b});
+            }
+            if (left.empty()) break;
+            if (K >= (long long)order.size()) {  // one cell per CTA already: keep the rest in CTAs of their own
+                for (int c : left) {
+                    bins.push_back({c});
+                    bin_n.push_back(usize[c]);
+                }
+                break;
+            }
         }
         // drop bins left empty (fewer units than CTAs)
         std::vector<std::vector<int>> kept;
@@ -339,38 +391,32 @@ std::string build_plan(const hx_group_desc& g, int nodes_per_warp, int max_pack_
     // Warps per cell and (balanced mode) the choice of cells per CTA follow an
     // estimate of a cell's forward + backward step time with w warps: the
     // latency of its Hines solve plus the per-node loops, whose time goes with
-    // the nodes each thread carries.  A cell whose branch segments fit its
-    // threads runs hines_rt, whose latency goes with the longest segment and
-    // the number of segment levels; other cells run hines_cell, whose latency
-    // goes with the level-by-level critical path (sum over levels of the
-    // longest segment) and the levels.  The constants are least-squares fits
-    // of per-cell clock64 timings of the forward + backward kernels on B200
+    // the nodes each thread carries.  The reduced-tree solve (hines_rt) goes
+    // with the longest segment times the segments a thread carries, plus the
+    // number of segment levels.  The constants are least-squares fits of
+    // per-cell clock64 timings of the forward + backward kernels on B200
     // (1024 config-2 cells, one wave; 2-3 % mean error); only their ratios
     // matter.  A CTA finishes with its slowest cell, so warps go one at a time
     // to the cell with the largest estimate, and in balanced mode cells are
     // moved / swapped out of the slowest CTA while that lowers its estimate.
     constexpr double kRtSeg = 662.0, kRtLevel = 2930.0, kRtIter = 10651.0;
-    constexpr double kHinesNode = 284.0, kHinesLevel = 3480.0, kNodeIter = 10930.0;
-    std::vector<double> uh_old(nunit, 0.0), uh_rt(nunit, 0.0);
+    std::vector<double> uh_seg(nunit, 0.0), uh_lvl(nunit, 0.0);
     std::vector<int> useg(nunit, 0);
     for (int u = 0; u < nunit; u++) {
-        std::map<int, int> longest;
+        std::set<int> levels;
         int maxseg = 0;
         for (const Branch& br : ubr[u]) {
-            int& l = longest[br.level];
-            l = std::max(l, (int)br.nodes.size());
+            levels.insert(br.level);
             maxseg = std::max(maxseg, (int)br.nodes.size());
         }
-        double crit = 0.0;
-        for (auto& kv : longest) crit += kv.second;
-        uh_old[u] = kHinesNode * crit + kHinesLevel * (double)longest.size();
-        uh_rt[u] = kRtSeg * maxseg + kRtLevel * (double)longest.size();
+        uh_seg[u] = kRtSeg * maxseg;
+        uh_lvl[u] = kRtLevel * (double)levels.size();
         useg[u] = (int)ubr[u].size();
     }
     auto unit_time = [&](int u, int w) {
         const double it = std::ceil((double)usize[u] / (32.0 * (double)w));
-        if (useg[u] <= 32 * w) return uh_rt[u] + kRtIter * it;
-        return uh_old[u] + kNodeIter * it;
+        const double per_thread = std::ceil((double)useg[u] / (32.0 * (double)w));
+        return uh_seg[u] * per_thread + uh_lvl[u] + kRtIter * it;
     };
     // greedy warps of one CTA; returns the CTA's estimate
     auto assign_warps = [&](const std::vector<int>& cs, std::vector<int>& w) {

@@ -276,18 +276,17 @@ int hx_load_group(hx_ctx* ctx, const hx_group_desc* desc) {
     ctx->probe_key.clear();
     ctx->tmid_steps = -1;
     // per-CTA node capacity from the opt-in shared memory: the forward kernel
-    // keeps 5 doubles per node (the backward 4) plus about 10 bytes of
-    // topology tables; network groups add 2 doubles per synapse of the pack,
-    // budgeted at 1.5x the group's mean synapse density.  A single cell larger
-    // than that is split across CTAs, whose kernels keep 10 doubles per node.
-    // The plan is checked against the exact table sizes and rebuilt with a
-    // smaller capacity while it does not fit.
+    // keeps 5 doubles per node (the backward 4) plus about 9 bytes of
+    // topology tables and the per-segment arrays (network groups keep their
+    // synapse states in global memory).  A single cell larger than that is
+    // split across CTAs, whose kernels keep 10 doubles per node.  The plan is
+    // checked against the exact table sizes and rebuilt with a capacity 1.5 %
+    // smaller while it does not fit: the step kernels are latency bound, so
+    // the nodes a wave of CTAs holds sets the throughput.
     int optin = 0, nsm = 0;
     HXC(cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, ctx->device));
     HXC(cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, ctx->device));
-    const double syn_per_node =
-        desc->nnode > 0 ? (double)(std::max(desc->nexpsyn, 0) + std::max(desc->nexp2syn, 0)) / desc->nnode : 0.0;
-    int cap_nodes = (int)((optin - 4096) / (5 * sizeof(double) + 12 + 1.5 * 16 * syn_per_node));
+    int cap_nodes = (int)((optin - 1024) / (5 * sizeof(double) + 8));
     bool split_kernels = false;
     if (desc->ncell == 1 && desc->nnode > cap_nodes) {
         split_kernels = true;
@@ -297,18 +296,8 @@ int hx_load_group(hx_ctx* ctx, const hx_group_desc* desc) {
     const int warps = split_kernels ? hx::kSplitThreads / 32 : hx::kWarpsPerCta;
     std::string e = hx::build_plan(*desc, ctx->pack_target, cap_nodes, ctx->P, nsm, warps);
     if (!e.empty()) return fail(ctx, "invalid group: " + e);
-    for (int shrink = 0; shrink < 24 && desc->nnode > 0; shrink++) {
-        // largest synapse count of any pack under this plan
+    for (int shrink = 0; shrink < 60 && desc->nnode > 0; shrink++) {
         const hx::Plan& Pc = ctx->P;
-        std::vector<int> nsyn_node(Pc.nnode, 0);
-        for (int i = 0; i < std::max(desc->nexpsyn, 0); i++) nsyn_node[Pc.ref2gpu[desc->expsyn_node[i]]]++;
-        for (int i = 0; i < std::max(desc->nexp2syn, 0); i++) nsyn_node[Pc.ref2gpu[desc->exp2syn_node[i]]]++;
-        int worst = 0;
-        for (int p = 0; p < Pc.npack; p++) {
-            int s = 0;
-            for (int gi = Pc.pack_node_off[p]; gi < Pc.pack_node_off[p + 1]; gi++) s += nsyn_node[gi];
-            worst = std::max(worst, s);
-        }
         hx::DevGroup Gt{};
         Gt.smem_n = std::max(Pc.max_pack_nodes, 1);
         Gt.smem_br = Pc.max_pack_branches;
@@ -316,9 +305,9 @@ int hx_load_group(hx_ctx* ctx, const hx_group_desc* desc) {
         Gt.smem_nch = Pc.max_pack_nch;
         Gt.smem_lvl = Pc.warps * (Pc.max_levels + 1);
         const size_t need = split_kernels ? std::max(hx::split_fwd_smem_bytes(Gt), hx::split_bwd_smem_bytes(Gt))
-                                          : std::max(hx::fwd_smem_bytes(Gt, worst), hx::bwd_smem_bytes(Gt, worst));
+                                          : std::max(hx::fwd_smem_bytes(Gt), hx::bwd_smem_bytes(Gt));
         if (need <= (size_t)optin) break;
-        cap_nodes = (int)(cap_nodes * 0.97);
+        cap_nodes = (int)(cap_nodes * 0.985);
         e = hx::build_plan(*desc, ctx->pack_target, cap_nodes, ctx->P, nsm, warps);
         if (!e.empty()) return fail(ctx, "invalid group: " + e);
     }
@@ -354,6 +343,20 @@ int hx_load_group(hx_ctx* ctx, const hx_group_desc* desc) {
     std::vector<int> flags(nn, 0);
     for (size_t gi = 0; gi < nn; gi++)
         flags[gi] = (P.node_pas[gi] >= 0 ? hx::kHasPas : 0) | (P.node_hh[gi] >= 0 ? hx::kHasHH : 0);
+    {  // network instances on / partners of each node (indices are validated by hx_net_load)
+        auto mark = [&](const int* node, int n, int bit) {
+            for (int i = 0; node && i < n; i++)
+                if (node[i] >= 0 && (size_t)node[i] < nn) flags[P.ref2gpu[node[i]]] |= bit;
+        };
+        mark(desc->expsyn_node, desc->nexpsyn, hx::kHasSyn);
+        mark(desc->exp2syn_node, desc->nexp2syn, hx::kHasSyn);
+        mark(desc->hg_node, desc->nhalfgap, hx::kHasCpl);
+        mark(desc->gj_node, desc->ngapj, hx::kHasCpl);
+        mark(desc->gr_node, desc->ngraded, hx::kHasCpl);
+        mark(desc->hg_src, desc->nhalfgap, hx::kHasIn);
+        mark(desc->gj_pre, desc->ngapj, hx::kHasIn);
+        mark(desc->gr_pre, desc->ngraded, hx::kHasIn);
+    }
     HXC(ctx->node_flags.upload(flags, st));
 
     // network tables (instance orders, kinds 8.. maps, device arrays)
@@ -478,7 +481,7 @@ int hx_load_group(hx_ctx* ctx, const hx_group_desc* desc) {
     if (ctx->split && ctx->lib) return fail(ctx, "library mechanisms on a cell split across CTAs are not supported");
     size_t sf = ctx->split ? hx::split_fwd_smem_bytes(G) : hx::fwd_smem_bytes(G);
     size_t sb = ctx->split ? hx::split_bwd_smem_bytes(G) : hx::bwd_smem_bytes(G);
-    size_t sfn = hx::fwd_smem_bytes(G, ctx->N.smem_syn), sbn = hx::bwd_smem_bytes(G, ctx->N.smem_syn);
+    size_t sfn = hx::fwd_smem_bytes(G), sbn = hx::bwd_smem_bytes(G);
     int maxsmem = 0;
     HXC(cudaDeviceGetAttribute(&maxsmem, cudaDevAttrMaxSharedMemoryPerBlockOptin, ctx->device));
     const size_t need = std::max(ctx->net ? std::max(sfn, sbn) : sb, sf);

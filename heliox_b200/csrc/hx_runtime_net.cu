@@ -149,9 +149,13 @@ int hx_net_load(hx_ctx* ctx, const hx_group_desc* d) {
     ctx->kmap_h[HX_P_EXPSYN_E] = ctx->kmap_h[HX_P_EXPSYN_W];
     ctx->kmap_h[HX_P_EXP2SYN_E] = ctx->kmap_h[HX_P_EXP2SYN_W];
     std::vector<int> nso = csr_by_node(so, nn), pso(P.npack + 1);
-    int smem_syn = 0;
     for (int p = 0; p <= P.npack; p++) pso[p] = nso[P.pack_node_off[p]];
-    for (int p = 0; p < P.npack; p++) smem_syn = std::max(smem_syn, pso[p + 1] - pso[p]);
+    // node and pack of every synapse (delivery by the node's owner thread,
+    // events bucketed per pack)
+    std::vector<int> snode(std::max(ns, 1), 0), spack(std::max(ns, 1), 0);
+    for (int j = 0; j < ns; j++) snode[j] = so[j].gnode;
+    for (int p = 0; p < P.npack; p++)
+        for (int j = pso[p]; j < pso[p + 1]; j++) spack[j] = p;
     std::vector<int> soff(ctx->nsrc + 1, 0), slist;
     for (int s = 0; s < ctx->nsrc; s++) {
         soff[s + 1] = soff[s] + (int)by_src[s].size();
@@ -160,6 +164,8 @@ int hx_net_load(hx_ctx* ctx, const hx_group_desc* d) {
     if (slist.empty()) slist.push_back(0);
     HXC(ctx->node_syn_off.upload(nso, st));
     HXC(ctx->pack_syn_off.upload(pso, st));
+    HXC(ctx->syn_node.upload(snode, st));
+    HXC(ctx->syn_pack.upload(spack, st));
     HXC(ctx->syn_kind.upload(kind, st));
     HXC(ctx->prm[HX_P_EXPSYN_E].upload(e, st));
     HXC(ctx->prm[HX_P_EXPSYN_W].upload(w, st));
@@ -267,7 +273,8 @@ int hx_net_load(hx_ctx* ctx, const hx_group_desc* d) {
 
     hx::DevNet& N = ctx->N;
     N.nsyn = ns;
-    N.smem_syn = smem_syn;
+    N.npack = P.npack;
+    N.syn_node = ctx->syn_node.p;
     N.node_syn_off = ctx->node_syn_off.p;
     N.pack_syn_off = ctx->pack_syn_off.p;
     N.syn_e = ctx->prm[HX_P_EXPSYN_E].p;
@@ -421,6 +428,7 @@ int hx_net_forward(hx_ctx* ctx, int nstep, double v_init, double* trace_dev, boo
     // process group's timeout then ends the peers' collective).
     const bool multi = ctx->exchange && ctx->nranks > 1;
     const int own_cap = ncell * ((W + 1) / 2) + 1;
+    const size_t nbucket = (size_t)std::max(nstep, 1) * (size_t)std::max(P.npack, 1);  // (step, pack) event buckets
     ctx->win_cap = ctx->win_cap_user > 0 ? ctx->win_cap_user : own_cap;
     HXC(ctx->win_send.ensure(ctx->win_cap));
     HXC(ctx->win_recv.ensure((size_t)ctx->win_cap * std::max(ctx->nranks, 1)));
@@ -435,8 +443,8 @@ int hx_net_forward(hx_ctx* ctx, int nstep, double v_init, double* trace_dev, boo
         if (capture && net_plan_tape(ctx, nstep, W)) return -1;
         ctx->log_cap = (int)std::min<long long>((long long)ncell * std::max(64, nstep / 20 + 1), 1LL << 26);
         HXC(ctx->spk_log.ensure(std::max(ctx->log_cap, 1)));
-        if (ctx->ev_cap == 0) ctx->ev_cap = ctx->nranks > 1 ? 1024 : 64;
-        HXC(ctx->ev_cnt.ensure(std::max(nstep, 1)));
+        if (ctx->ev_cap == 0) ctx->ev_cap = 16;
+        HXC(ctx->ev_cnt.ensure(nbucket));
         return 0;
     };
     bool ok = setup() == 0;
@@ -445,14 +453,14 @@ int hx_net_forward(hx_ctx* ctx, int nstep, double v_init, double* trace_dev, boo
     hx::DevProbe PV = hx_probe_view(ctx);
     const double half_dt = ctx->dt / 2;
     for (int attempt = 0; attempt < 6; attempt++) {
-        if (ok && ctx->ev_syn.ensure((size_t)std::max(nstep, 1) * ctx->ev_cap) != cudaSuccess) {
+        if (ok && ctx->ev_syn.ensure(nbucket * ctx->ev_cap) != cudaSuccess) {
             hx_fail(ctx, "event bucket allocation failed");
             if (!multi) return -1;
             ok = false;
             local_err = ctx->err;
         }
         auto init_attempt = [&]() -> int {
-            HXC(cudaMemsetAsync(ctx->ev_cnt.p, 0, (size_t)std::max(nstep, 1) * 4, st));
+            HXC(cudaMemsetAsync(ctx->ev_cnt.p, 0, nbucket * 4, st));
             HXC(cudaMemsetAsync(ctx->dev_err.p, 0, 4, st));
             HXC(cudaMemsetAsync(ctx->log_n.p, 0, 4, st));
             HXC(cudaMemsetAsync(ctx->cs_ps_flag.p, 0, (size_t)std::max(ncell, 1) * 4, st));
@@ -464,8 +472,8 @@ int hx_net_forward(hx_ctx* ctx, int nstep, double v_init, double* trace_dev, boo
             if (attempt == 0) HXC(cudaEventRecord(ctx->ev[0], st));
             if (ctx->nsyn && ctx->ns_count)
                 HXC(hx::launch_route(ctx->ns_spk.p, nullptr, ctx->ns_count, ctx->src_off.p, ctx->src_syn.p,
-                                     ctx->nsrc, ctx->syn_delay.p, ctx->tstart.p, nstep, half_dt, 0, ctx->ev_cnt.p,
-                                     ctx->ev_syn.p, ctx->ev_cap, ctx->dev_err.p, st));
+                                     ctx->nsrc, ctx->syn_delay.p, ctx->tstart.p, nstep, half_dt, 0, ctx->syn_pack.p,
+                                     P.npack, ctx->ev_cnt.p, ctx->ev_syn.p, ctx->ev_cap, ctx->dev_err.p, st));
             return 0;
         };
         int launches = 0;
@@ -503,8 +511,8 @@ int hx_net_forward(hx_ctx* ctx, int nstep, double v_init, double* trace_dev, boo
         };
         auto route_window = [&](const int2* spk, const int* nspk, int nmax, int k1) -> int {
             HXC(hx::launch_route(spk, nspk, nmax, ctx->src_off.p, ctx->src_syn.p, ctx->nsrc, ctx->syn_delay.p,
-                                 ctx->tstart.p, nstep, half_dt, k1, ctx->ev_cnt.p, ctx->ev_syn.p, ctx->ev_cap,
-                                 ctx->dev_err.p, st));
+                                 ctx->tstart.p, nstep, half_dt, k1, ctx->syn_pack.p, P.npack, ctx->ev_cnt.p,
+                                 ctx->ev_syn.p, ctx->ev_cap, ctx->dev_err.p, st));
             launches++;
             return 0;
         };
@@ -540,7 +548,7 @@ int hx_net_forward(hx_ctx* ctx, int nstep, double v_init, double* trace_dev, boo
         int err = 0, need = 0, bad_rank = -1;
         if (multi) {
             // every rank's (error bits, largest bucket count) after its last window
-            if (ok && hx::launch_net_status(ctx->dev_err.p, ctx->ev_cnt.p, nstep, 0, ctx->st_send.p, st) !=
+            if (ok && hx::launch_net_status(ctx->dev_err.p, ctx->ev_cnt.p, (int)nbucket, 0, ctx->st_send.p, st) !=
                           cudaSuccess) {
                 ok = false;
                 local_err = "status kernel launch failed";
@@ -571,7 +579,7 @@ int hx_net_forward(hx_ctx* ctx, int nstep, double v_init, double* trace_dev, boo
         if (err & HX_XS_WINDOW) return hx_fail(ctx, "window spike buffer overflow");
         if (err & HX_XS_BUCKET) {
             if (!multi) {
-                std::vector<int> cnt(std::max(nstep, 1));
+                std::vector<int> cnt(nbucket);
                 HXC(cudaMemcpy(cnt.data(), ctx->ev_cnt.p, cnt.size() * 4, cudaMemcpyDeviceToHost));
                 need = *std::max_element(cnt.begin(), cnt.end());
             }

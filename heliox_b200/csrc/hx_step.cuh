@@ -220,154 +220,104 @@ __device__ __forceinline__ bool setup_pack(const DevGroup& G, int p, int* ibase,
     return false;
 }
 
-template <bool kTransposed>
-__device__ __forceinline__ void hines_cell(const Meta& M, const Grp& g, const double* __restrict__ sa,
-                                           const double* __restrict__ sb, double* __restrict__ d,
-                                           double* __restrict__ rhs) {
-    const double* __restrict__ A = kTransposed ? sb : sa;
-    const double* __restrict__ U = kTransposed ? sa : sb;
-    const int* lo = M.lvl + g.lvl;
-    for (int L = g.nlev - 1; L >= 0; --L) {
-        const int b1 = lo[L + 1];
-        for (int br = lo[L] + g.tl; br < b1; br += g.nt) {
-            const int h = M.bh[br], e = M.be[br];
-            double de = d[e], re = rhs[e];
-            // child branches fold into the end node (d[c] = 1/d'_c, rhs[c] = r'_c/d'_c)
-            const int c1 = M.bco[br + 1];
-            for (int k = M.bco[br]; k < c1; ++k) {
-                const int c = M.bc[k];
-                de = __fma_rn(-(A[c] * U[c]), d[c], de);
-                re = __fma_rn(-A[c], rhs[c], re);
-            }
-            double pp = de, qq = 1.0, yy = re;
-            int j = e;
-            for (; j - h >= kBlk; j -= kBlk) {
-                tri_block<false>(d, rhs, A, U, j, kBlk, pp, qq, yy);
-                const double s = rescale_pow2(pp);
-                pp *= s;
-                qq *= s;
-                yy *= s;
-            }
-            if (j > h) tri_block<true>(d, rhs, A, U, j, j - h, pp, qq, yy);
-            const double ip = rcp_nz(pp);
-            d[h] = qq * ip;
-            rhs[h] = yy * ip;
-        }
-        g.sync();
-    }
-    for (int L = 0; L < g.nlev; ++L) {
-        const int b1 = lo[L + 1];
-        for (int br = lo[L] + g.tl; br < b1; br += g.nt) {
-            const int h = M.bh[br], e = M.be[br];
-            const int par = M.bp[br];
-            double x = rhs[h];
-            if (par >= 0) x = __fma_rn(-(U[h] * d[h]), rhs[par], x);
-            rhs[h] = x;
-            int j = h + 1;
-            for (; e - j + 1 >= kBlk; j += kBlk) back_block<false>(d, rhs, U, j, kBlk, x);
-            if (j <= e) back_block<true>(d, rhs, U, j, e - j + 1, x);
-        }
-        g.sync();
-    }
-}
-
-// hines_rt: the same solve as hines_cell in three phases, for a cell with at
-// most one branch segment per thread (thread tl owns segment lo[0] + tl in
-// every phase, so a segment's fill couplings stay in its registers):
+// hines_rt: Hines solve of one cell's system by its warp group, in three
+// phases over the cell's branch segments (a branch cut into pieces of at
+// most kSegMax nodes; segments sorted by level, lo[L] .. lo[L+1] the segments
+// of level L):
 //  1. every segment eliminates its interior nodes h .. e-1 top-down, keeping
 //     its head's parent P and its end e: d[k] := 1/D'_k on the interior, the
-//     end's diagonal / rhs updated in place, and the fill couplings P-e (Fe in
-//     P's row, Ge in e's row) and the interior's contributions to P's
-//     diagonal / rhs (dD, dR) kept;
+//     end's diagonal / rhs updated in place, the fill couplings P-e (fe in
+//     P's row, ge in e's row) and the interior's contributions to P's
+//     diagonal / rhs (dD, dR) kept per segment;
 //  2. the tree of segment ends is solved level by level: an end folds in its
-//     child segments' contributions cd, cr (their dD + Fe Ge / D_e, dR +
-//     Fe R_e / D_e), then x_e = R_e/D_e - (Ge/D_e) x_P root-first;
+//     child segments' contributions cd, cr (their dD + fe ge / D_e, dR +
+//     fe R_e / D_e), then x_e = R_e/D_e - (ge/D_e) x_P root-first;
 //  3. every segment solves its interior from x_P and x_e (forward r'' sweep,
 //     then back-substitution).
-// The serial depth is the longest segment (at most kSegMax nodes) twice plus
-// the number of levels, instead of the longest branch of every level.  cd, cr:
-// one double per branch of the pack each.  The elimination order differs from
-// the reference's, so results agree to rounding (the CPU replay of this form
-// is checked against solve_serial by hx_plan_check).
+// Thread tl takes segments lo[0] + tl + m nt in phases 1 and 3 and the
+// level's segments lo[L] + tl + m nt in phase 2, so a cell with more
+// segments than threads (a large cell on one warp) keeps this form; every
+// segment's arithmetic is the same whichever thread does it.  The serial
+// depth is the longest segment twice (times the segments a thread carries)
+// plus the number of levels, instead of the longest branch of every level.
+// cd, cr, fe, ge: one double per segment of the pack each.  The elimination
+// order differs from the reference's, so results agree to rounding (the CPU
+// replay of this form is checked against solve_serial by hx_plan_check).
 template <bool kTransposed>
 __device__ __forceinline__ void hines_rt(const Meta& M, const Grp& g, const double* __restrict__ sa,
                                          const double* __restrict__ sb, double* __restrict__ d,
-                                         double* __restrict__ rhs, double* __restrict__ cd, double* __restrict__ cr) {
+                                         double* __restrict__ rhs, double* __restrict__ cd, double* __restrict__ cr,
+                                         double* __restrict__ fe, double* __restrict__ ge) {
     const double* __restrict__ A = kTransposed ? sb : sa;
     const double* __restrict__ U = kTransposed ? sa : sb;
     const int* lo = M.lvl + g.lvl;
-    const int s = lo[0] + g.tl;
-    const bool own = s < lo[g.nlev];
-    int h = 0, e = -1, P = -1, Ls = -1;
-    double Fe = 0.0, Ge = 0.0;
-    if (own) {
-        h = M.bh[s];
-        e = M.be[s];
-        P = M.bp[s];
-        Ls = 0;
-        while (lo[Ls + 1] <= s) ++Ls;
+    const int s_end = lo[g.nlev];
+    for (int s = lo[0] + g.tl; s < s_end; s += g.nt) {
+        const int h = M.bh[s], e = M.be[s];
         if (h == e) {
-            Fe = A[h];
-            Ge = U[h];
+            fe[s] = A[h];
+            ge[s] = U[h];
             cd[s] = 0.0;
             cr[s] = 0.0;
-        } else {
-            double inv = rcp_nz(d[h]);
-            double rp = rhs[h];
-            double F = A[h], G = U[h];
-            double dD = F * G * inv, dR = F * rp * inv;
-            d[h] = inv;
-            // interior nodes h+1 .. e-1 in register blocks: operands loaded
-            // ahead of the dependent arithmetic, results stored after it
-            int k = h + 1;
-            for (; k + kBlk <= e; k += kBlk) {
-                double uk[kBlk], ak[kBlk], dk[kBlk], rk[kBlk], iv[kBlk];
-#pragma unroll
-                for (int u = 0; u < kBlk; ++u) {
-                    uk[u] = U[k + u];
-                    ak[u] = A[k + u];
-                    dk[u] = d[k + u];
-                    rk[u] = rhs[k + u];
-                }
-#pragma unroll
-                for (int u = 0; u < kBlk; ++u) {
-                    const double Dk = __fma_rn(-(uk[u] * ak[u]), inv, dk[u]);
-                    const double rn = __fma_rn(-(uk[u] * rp), inv, rk[u]);
-                    F = -(F * ak[u]) * inv;
-                    G = -(uk[u] * G) * inv;
-                    inv = rcp_nz(Dk);
-                    rp = rn;
-                    dD = __fma_rn(F * G, inv, dD);
-                    dR = __fma_rn(F * rp, inv, dR);
-                    iv[u] = inv;
-                }
-#pragma unroll
-                for (int u = 0; u < kBlk; ++u) d[k + u] = iv[u];
-            }
-            for (; k < e; ++k) {
-                const double Uk = U[k], Ak = A[k];
-                const double Dk = __fma_rn(-(Uk * Ak), inv, d[k]);
-                const double rk = __fma_rn(-(Uk * rp), inv, rhs[k]);
-                F = -(F * Ak) * inv;
-                G = -(Uk * G) * inv;
-                inv = rcp_nz(Dk);
-                rp = rk;
-                dD = __fma_rn(F * G, inv, dD);
-                dR = __fma_rn(F * rp, inv, dR);
-                d[k] = inv;
-            }
-            const double Ue = U[e], Ae = A[e];
-            d[e] = __fma_rn(-(Ue * Ae), inv, d[e]);
-            rhs[e] = __fma_rn(-(Ue * rp), inv, rhs[e]);
-            Fe = -(F * Ae) * inv;
-            Ge = -(Ue * G) * inv;
-            cd[s] = dD;
-            cr[s] = dR;
+            continue;
         }
+        double inv = rcp_nz(d[h]);
+        double rp = rhs[h];
+        double F = A[h], Gc = U[h];
+        double dD = F * Gc * inv, dR = F * rp * inv;
+        d[h] = inv;
+        // interior nodes h+1 .. e-1 in register blocks: operands loaded
+        // ahead of the dependent arithmetic, results stored after it
+        int k = h + 1;
+        for (; k + kBlk <= e; k += kBlk) {
+            double uk[kBlk], ak[kBlk], dk[kBlk], rk[kBlk], iv[kBlk];
+#pragma unroll
+            for (int u = 0; u < kBlk; ++u) {
+                uk[u] = U[k + u];
+                ak[u] = A[k + u];
+                dk[u] = d[k + u];
+                rk[u] = rhs[k + u];
+            }
+#pragma unroll
+            for (int u = 0; u < kBlk; ++u) {
+                const double Dk = __fma_rn(-(uk[u] * ak[u]), inv, dk[u]);
+                const double rn = __fma_rn(-(uk[u] * rp), inv, rk[u]);
+                F = -(F * ak[u]) * inv;
+                Gc = -(uk[u] * Gc) * inv;
+                inv = rcp_nz(Dk);
+                rp = rn;
+                dD = __fma_rn(F * Gc, inv, dD);
+                dR = __fma_rn(F * rp, inv, dR);
+                iv[u] = inv;
+            }
+#pragma unroll
+            for (int u = 0; u < kBlk; ++u) d[k + u] = iv[u];
+        }
+        for (; k < e; ++k) {
+            const double Uk = U[k], Ak = A[k];
+            const double Dk = __fma_rn(-(Uk * Ak), inv, d[k]);
+            const double rk = __fma_rn(-(Uk * rp), inv, rhs[k]);
+            F = -(F * Ak) * inv;
+            Gc = -(Uk * Gc) * inv;
+            inv = rcp_nz(Dk);
+            rp = rk;
+            dD = __fma_rn(F * Gc, inv, dD);
+            dR = __fma_rn(F * rp, inv, dR);
+            d[k] = inv;
+        }
+        const double Ue = U[e], Ae = A[e];
+        d[e] = __fma_rn(-(Ue * Ae), inv, d[e]);
+        rhs[e] = __fma_rn(-(Ue * rp), inv, rhs[e]);
+        fe[s] = -(F * Ae) * inv;
+        ge[s] = -(Ue * Gc) * inv;
+        cd[s] = dD;
+        cr[s] = dR;
     }
     g.sync();
     for (int L = g.nlev - 1; L >= 0; --L) {
-        if (Ls == L) {
+        const int l1 = lo[L + 1];
+        for (int s = lo[L] + g.tl; s < l1; s += g.nt) {
+            const int e = M.be[s];
             double De = d[e], Re = rhs[e];
             const int c1 = M.bco[s + 1];
             for (int k = M.bco[s]; k < c1; ++k) {
@@ -376,23 +326,28 @@ __device__ __forceinline__ void hines_rt(const Meta& M, const Grp& g, const doub
                 Re -= cr[c];
             }
             const double ie = rcp_nz(De);
-            const double ge = Re * ie, he = Ge * ie;
-            cd[s] = __fma_rn(Fe, he, cd[s]);
-            cr[s] = __fma_rn(Fe, ge, cr[s]);
+            const double gv = Re * ie, he = ge[s] * ie;
+            const double f = fe[s];
+            cd[s] = __fma_rn(f, he, cd[s]);
+            cr[s] = __fma_rn(f, gv, cr[s]);
             d[e] = he;
-            rhs[e] = ge;
+            rhs[e] = gv;
         }
         g.sync();
     }
     for (int L = 0; L < g.nlev; ++L) {
-        if (Ls == L) {
+        const int l1 = lo[L + 1];
+        for (int s = lo[L] + g.tl; s < l1; s += g.nt) {
+            const int e = M.be[s], P = M.bp[s];
             double x = rhs[e];
             if (P >= 0) x = __fma_rn(-d[e], rhs[P], x);
             rhs[e] = x;
         }
         g.sync();
     }
-    if (own && h < e) {
+    for (int s = lo[0] + g.tl; s < s_end; s += g.nt) {
+        const int h = M.bh[s], e = M.be[s], P = M.bp[s];
+        if (h >= e) continue;
         double t = rhs[h];
         if (P >= 0) t = __fma_rn(-U[h], rhs[P], t);
         t *= d[h];
@@ -444,11 +399,6 @@ __device__ __forceinline__ void hines_rt(const Meta& M, const Grp& g, const doub
     g.sync();
 }
 
-// Segments of the group's cell fit its threads (hines_rt applies).
-__device__ __forceinline__ bool rt_fits(const Meta& M, const Grp& g) {
-    return M.lvl[g.lvl + g.nlev] - M.lvl[g.lvl] <= g.nt;
-}
-
 // ------------------------------------------------------------------ per-step I/O
 // dst[i] = src[i] for the group's nodes i = i0 + tl + j*nt, four loads in flight
 // per thread before the stores.
@@ -494,11 +444,12 @@ __device__ __forceinline__ void probe_inject(const DevProbe& P, int q0, int q1, 
 
 // ------------------------------------------------------------------ assembly
 // One point-process contribution through MechTemp::current
-// (mech_template.cuh:612-645): i1 = I(v+0.001), i0 = I(v), scaled by 1e2/area.
-__device__ __forceinline__ void pp_add(double i1, double i0, double area, bool electrode, double& r, double& dd) {
+// (mech_template.cuh:612-645): i1 = I(v+0.001), i0 = I(v), scaled by
+// sarea = 1e2/area (the node's quotient, computed once per node and step).
+__device__ __forceinline__ void pp_add(double i1, double i0, double sarea, bool electrode, double& r, double& dd) {
     double gg = (i1 - i0) * kInvFdEps;
-    gg *= 1.e2 / area;
-    i0 *= 1.e2 / area;
+    gg *= sarea;
+    i0 *= sarea;
     if (electrode) {
         r += i0;
         dd -= gg;
@@ -513,31 +464,77 @@ __device__ __forceinline__ void pp_add(double i1, double i0, double area, bool e
 // (HalfGap.cu:56-62, electrode), gapjunction_lr (gapjunction_lr.cu:58-65),
 // neuron_to_neuron_syn_lr (neuron_to_neuron_syn_lr.cu:120-127).  synA/synB are
 // the cell's synapse states indexed from syn0; grs the graded states s_k.
-__device__ __forceinline__ void assemble_net(const DevGroup& G, const DevNet& N, int gi, double vi,
-                                             const double* __restrict__ synA, const double* __restrict__ synB,
-                                             int syn0, const double* __restrict__ grs,
-                                             const double* __restrict__ vpeer, double& r, double& dd) {
-    const double area = __ldg(G.area + gi);
-    const int s1 = __ldg(N.node_syn_off + gi + 1);
-    for (int j = __ldg(N.node_syn_off + gi); j < s1; ++j) {
-        const double gs = synB[j - syn0] - synA[j - syn0], e = __ldg(N.syn_e + j);
-        pp_add(gs * ((vi + kFdEps) - e), gs * (vi - e), area, false, r, dd);
+// A node's synapse range and its first synapse's states and reversal
+// potential, loaded at the top of a node iteration (load_syn, next to
+// load_par) so that their latency overlaps the mechanism arithmetic instead of
+// adding a dependent round trip where the current is assembled.
+struct SynPre {
+    int s0 = 0, s1 = 0;
+    double A0 = 0.0, B0 = 0.0, E0 = 0.0, sarea = 1.0;
+};
+
+// The synapse range of the node a thread takes next (pack-local node i, i >=
+// i1: none), loaded one iteration ahead so that load_syn finds it ready.
+struct SynNext {
+    int s0 = 0, s1 = 0;
+    double sarea = 1.0;  // 1e2 / the node's area (network nodes)
+};
+
+__device__ __forceinline__ void syn_next(const DevGroup& G, const DevNet& N, const Meta& M, int pb, int i, int i1,
+                                         SynNext& nx) {
+    nx.s0 = nx.s1 = 0;
+    if (i >= i1) return;
+    const int fl = M.flag[i];
+    if (fl & kHasSyn) {
+        nx.s0 = __ldg(N.node_syn_off + pb + i);
+        nx.s1 = __ldg(N.node_syn_off + pb + i + 1);
     }
-    if (!N.coupled) return;
+    if (fl & (kHasSyn | kHasCpl)) nx.sarea = 1.e2 / __ldg(G.area + pb + i);
+}
+
+__device__ __forceinline__ void load_syn(const DevNet& N, const SynNext& nx, const double* __restrict__ synA,
+                                         const double* __restrict__ synB, SynPre& sp) {
+    sp.s0 = nx.s0;
+    sp.s1 = nx.s1;
+    sp.sarea = nx.sarea;
+    if (sp.s0 < sp.s1) {
+        sp.A0 = synA[sp.s0];
+        sp.B0 = synB[sp.s0];
+        sp.E0 = __ldg(N.syn_e + sp.s0);
+    }
+}
+
+template <bool kCpl>
+__device__ __forceinline__ void assemble_net(const DevGroup& G, const DevNet& N, int gi, int fl, double vi,
+                                             const double* __restrict__ synA, const double* __restrict__ synB,
+                                             const SynPre& sp, const double* __restrict__ grs,
+                                             const double* __restrict__ vpeer, double& r, double& dd) {
+    if (!(fl & (kHasSyn | kHasCpl))) return;
+    const double sarea = sp.sarea;
+    if (fl & kHasSyn) {
+        double gs = sp.B0 - sp.A0, e = sp.E0;
+        pp_add(gs * ((vi + kFdEps) - e), gs * (vi - e), sarea, false, r, dd);
+        for (int j = sp.s0 + 1; j < sp.s1; ++j) {
+            gs = synB[j] - synA[j];
+            e = __ldg(N.syn_e + j);
+            pp_add(gs * ((vi + kFdEps) - e), gs * (vi - e), sarea, false, r, dd);
+        }
+    }
+    if (!kCpl || !(fl & kHasCpl)) return;
     const int h1 = __ldg(N.node_hg_off + gi + 1);
     for (int j = __ldg(N.node_hg_off + gi); j < h1; ++j) {
         const double vg = vpeer[__ldg(N.hg_src + j)], g = __ldg(N.hg_g + j);
-        pp_add((vg - (vi + kFdEps)) * g, (vg - vi) * g, area, true, r, dd);
+        pp_add((vg - (vi + kFdEps)) * g, (vg - vi) * g, sarea, true, r, dd);
     }
     const int j1 = __ldg(N.node_gj_off + gi + 1);
     for (int j = __ldg(N.node_gj_off + gi); j < j1; ++j) {
         const double vp = vpeer[__ldg(N.gj_pre + j)], g = __ldg(N.gj_g + j), w = __ldg(N.gj_w + j);
-        pp_add(w * (g * ((vi + kFdEps) - vp)), w * (g * (vi - vp)), area, false, r, dd);
+        pp_add(w * (g * ((vi + kFdEps) - vp)), w * (g * (vi - vp)), sarea, false, r, dd);
     }
     const int r1 = __ldg(N.node_gr_off + gi + 1);
     for (int j = __ldg(N.node_gr_off + gi); j < r1; ++j) {
         const double aw = fabs(__ldg(N.gr_w + j)), gs = __ldg(N.gr_g + j) * grs[j], er = __ldg(N.gr_erev + j);
-        pp_add(aw * (gs * ((vi + kFdEps) - er)), aw * (gs * (vi - er)), area, false, r, dd);
+        pp_add(aw * (gs * ((vi + kFdEps) - er)), aw * (gs * (vi - er)), sarea, false, r, dd);
     }
 }
 
@@ -652,13 +649,14 @@ __device__ __forceinline__ double vjp_mech(const DevGroup& G, const DevGrad& GR,
 // channels; *ica receives the node's calcium current], capacitance
 // jacobian, axial terms.  vi is the node's voltage; sv (neighbour voltages) is
 // read only when kRhs.
-template <bool kRhs, bool kNet = false, bool kSplitAxial = false, bool kLib = false>
+template <bool kRhs, bool kNet = false, bool kSplitAxial = false, bool kLib = false, bool kCpl = false>
 __device__ __forceinline__ void assemble(const DevGroup& G, const Meta& M, int pb, int i, int fl, const NodePar& q,
                                          double vi, const double* __restrict__ sv, const double* __restrict__ sa,
                                          const double* __restrict__ sb, double m, double h, double n, double tmid,
                                          double& r_out, double& d_out, const DevNet& N = DevNet{},
-                                         const double* synA = nullptr, const double* synB = nullptr, int syn0 = 0,
-                                         const double* grs = nullptr, const double* vpeer = nullptr,
+                                         const double* synA = nullptr, const double* synB = nullptr,
+                                         const SynPre& sp = SynPre{}, const double* grs = nullptr,
+                                         const double* vpeer = nullptr,
                                          const DevLib* L = nullptr, const double* X = nullptr,
                                          double* ica = nullptr) {
     const int gi = pb + i;
@@ -683,7 +681,7 @@ __device__ __forceinline__ void assemble(const DevGroup& G, const Meta& M, int p
         const double cur = (tmid < del + dur && tmid >= del) ? __ldg(G.ic_amp + j) : 0.0;
         r += cur * (1.e2 / __ldg(G.area + gi));
     }
-    if (kNet) assemble_net(G, N, gi, vi, synA, synB, syn0, grs, vpeer, r, dd);
+    if (kNet) assemble_net<kCpl>(G, N, gi, fl, vi, synA, synB, sp, grs, vpeer, r, dd);
     if (kLib) *ica = lib::lib_current(*L, gi, vi, X, r, dd);  // library types follow the network ones
     dd += G.cfac * q.cm;
     if (kSplitAxial) {  // parent / children may sit in other CTAs (a split cell)
