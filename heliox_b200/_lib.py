@@ -187,6 +187,7 @@ SIGNATURES = {
     "hx_mse_loss_grad_noalloc": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_void_p, C.c_void_p,
                                             C.c_void_p]),
     "hx_last_kernel_ms": (C.c_int, [C.c_void_p, C.c_int, _dp, _ip]),
+    "hx_rcp_nz_dev": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int, C.c_void_p]),
     "hx_opt_create_adam": (C.c_int, [C.c_void_p, C.c_double, C.c_double, C.c_double]),
     "hx_opt_add_params": (C.c_int, [C.c_void_p, C.c_int, C.c_int, _ip, _ip, C.c_double]),
     "hx_opt_set_grads_f32": (C.c_int, [C.c_void_p, C.c_int, _fp, C.c_int]),

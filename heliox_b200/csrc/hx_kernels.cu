@@ -1,21 +1,26 @@
 // hx_kernels.cu -- fused per-timestep kernels for sm_100a (fp64).
 //
-// One CTA owns one cell pack for a whole window of timesteps: voltages, the
-// Hines work arrays, the hh gates and the pack's topology/schedule tables stay
-// in shared memory across steps; only the forward tape, the recorded probes and
-// the node parameters (L2-resident) touch global memory inside the loop.  Each
-// cell of the pack is advanced by its own group of warps, synchronised by a
-// named barrier, so the serial parts of one cell's Hines solve overlap the
-// mechanism arithmetic of the other cells on the same SM.
+// One CTA owns one pack of whole cells for a launch's window of timesteps
+// (one CTA per SM; the planner packs cells so that as few waves as the shared
+// memory allows hold them).  Shared memory holds only what neighbouring nodes
+// exchange: the Hines system (v, rhs, d, a, b in the forward; w, d, a, b in the
+// reverse sweep), four doubles per branch segment for the reduced-tree solve
+// and the pack's topology tables.  Gates, node adjoints, gradient
+// accumulators, synapse states and parameters live in global memory (L2), each
+// read and written only by the thread that owns the node.  Each cell is
+// advanced by its own group of warps, synchronised by a named barrier, so the
+// serial parts of one cell's Hines solve overlap the mechanism arithmetic of
+// the other cells on the same SM.
 //
 // Forward step (reference: Simulate::fadvance_cpu, src/simulate.cpp:410-442):
-//   A  node-parallel: mechanism currents with the finite-difference
-//      conductance (mech_template.cuh:589-648), capacitance jacobian
-//      (capac.cpp:68-78) and the axial terms (simulate.cpp:542-555) gathered
-//      per node in the order the reference's scatter loop applies them;
-//   B  Hines solve on the branch-level schedule (hines_smem below);
-//   C  v += dv (update_cpu, simulate.cpp:759-770), then the hh cnexp state
-//      update at the new voltage (nonvint_cpu, simulate.cpp:784-852).
+//   A  node-parallel: the gates' cnexp update from v_k (nonvint_cpu,
+//      simulate.cpp:784-852, applied one step late so the gates are read once
+//      a step), mechanism currents with the finite-difference conductance
+//      (mech_template.cuh:589-648), capacitance jacobian (capac.cpp:68-78)
+//      and the axial terms (simulate.cpp:542-555) gathered per node in the
+//      order the reference's scatter loop applies them;
+//   B  Hines solve by segments (hines_rt, hx_step.cuh);
+//   C  v += dv (update_cpu, simulate.cpp:759-770).
 // Backward step: the transpose of the above, in reverse (no reference
 // counterpart; the reference's only gradient is the LRDS replay).
 #include <cuda_runtime.h>
@@ -870,6 +875,18 @@ __global__ void net_status_kernel(const int* __restrict__ err, const int* __rest
         __syncthreads();
     }
     if (threadIdx.x == 0) *out = make_int2(*err | extra, red[0]);
+}
+
+// The library's reciprocal over an array (verification of rcp_nz against IEEE division)
+__global__ void rcp_nz_kernel(const double* __restrict__ x, double* __restrict__ y, int n) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < n) y[i] = rcp_nz(x[i]);
+}
+
+cudaError_t launch_rcp_nz(const double* x, double* y, int n, cudaStream_t st) {
+    if (n <= 0) return cudaSuccess;
+    rcp_nz_kernel<<<(n + 255) / 256, 256, 0, st>>>(x, y, n);
+    return cudaGetLastError();
 }
 
 cudaError_t launch_net_status(const int* err, const int* ev_cnt, int nstep, int extra, int2* out, cudaStream_t st) {

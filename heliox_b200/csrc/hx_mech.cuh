@@ -60,12 +60,35 @@ __device__ __forceinline__ ZPow zpow(double v) {
     return ZPow{z9, z36, z36 * z4, z36 * z36};
 }
 
+// Below this |u| = |x/10| the vtrap forms take exp(u) from a direct exp
+// instead of the z powers (whose ~72 ulp would dominate exp(u) - 1 there), and
+// the derivative's numerator from its series.
+constexpr double kVtrapNear = 0.05;
+
 // vtrap(x, 10) = x / (exp(x/10) - 1) with exp(x/10) given; the reference's
 // small-argument branch (hh_templated.cu:76-85) is kept
 __device__ __forceinline__ double vtrap10_e(double x, double ex) {
     const double u = x * 0.1;
     if (fabs(u) < 1e-6) return 10.0 * (1 - u * 0.5);
+    if (fabs(u) < kVtrapNear) ex = exp(u);
     return x * rcp_nz(ex - 1);
+}
+
+// (exp(u) - 1 - u exp(u)) = -sum_{n>=2} (n-1) u^n / n!, for |u| < kVtrapNear
+// (terms to n = 11: below double rounding there), free of the cancellation
+// of the direct difference
+__device__ __forceinline__ double vtrap_num_series(double u) {
+    double t = 10.0 / 39916800.0;                 // n = 11: (n-1)/n!, Horner in u down to n = 2
+    t = t * u + 9.0 / 3628800.0;                  // n = 10
+    t = t * u + 8.0 / 362880.0;                   // n = 9
+    t = t * u + 7.0 / 40320.0;                    // n = 8
+    t = t * u + 6.0 / 5040.0;                     // n = 7
+    t = t * u + 5.0 / 720.0;                      // n = 6
+    t = t * u + 4.0 / 120.0;                      // n = 5
+    t = t * u + 3.0 / 24.0;                       // n = 4
+    t = t * u + 2.0 / 6.0;                        // n = 3
+    t = t * u + 1.0 / 2.0;                        // n = 2
+    return -(u * u) * t;
 }
 
 __device__ __forceinline__ void hh_rates(double v, double q10, HHRates& r) {
@@ -94,6 +117,11 @@ __device__ __forceinline__ void vtrap10_d_e(double x, double ex, double& f, doub
     if (fabs(u) < 1e-6) {
         f = 10.0 * (1 - u * 0.5);
         df = -0.5;
+    } else if (fabs(u) < kVtrapNear) {
+        ex = exp(u);
+        f = x * rcp_nz(ex - 1);
+        const double r = rcp_nz(expm1(u));
+        df = vtrap_num_series(u) * (r * r);
     } else {
         const double em1 = ex - 1;
         const double r = rcp_nz(em1);

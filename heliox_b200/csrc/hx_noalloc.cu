@@ -24,8 +24,11 @@ constexpr int kMaxDevices = 64;
 
 static __device__ __align__(256) double g_mse_scratch[kMaxPartials];
 
-// Host-side stand-in of the scratch array resolved to its device address, per
-// device (the symbol's name is not a device address in host code).
+// The scratch array's device address per device (in host code the symbol's
+// name is a host-side stand-in, not a device address).  Resolved again on
+// every call made outside stream capture, so an address a cudaDeviceReset
+// made stale is never used; a call during capture uses the address resolved
+// by the device's last call outside capture.
 double* g_scratch_ptr[kMaxDevices] = {nullptr};
 std::mutex g_scratch_mu;
 
@@ -85,23 +88,29 @@ extern "C" int hx_mse_loss_grad_noalloc(const double* trace_dev, const double* t
                 n, (long long)kMaxPartials * kChunk, kMaxPartials, kChunk);
         return -2;
     }
+    // an error left by earlier work is the caller's to read: report it
+    // without clearing it and without doing any work
+    if (cudaPeekAtLastError() != cudaSuccess) return -4;
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return -3;
+    cudaStream_t st = (cudaStream_t)stream;
+    cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+    if (cudaStreamIsCapturing(st, &cap) != cudaSuccess) return -3;
     double* scratch = nullptr;
     {
-        // first call on a device: resolve the scratch array's device address
         std::lock_guard<std::mutex> lock(g_scratch_mu);
-        if (!g_scratch_ptr[dev]) {
+        if (cap == cudaStreamCaptureStatusNone) {  // (re)resolve the scratch array's device address
             double* p = nullptr;
             if (cudaGetSymbolAddress((void**)&p, g_mse_scratch) != cudaSuccess || !p) return -3;
             g_scratch_ptr[dev] = p;
         }
         scratch = g_scratch_ptr[dev];
     }
-    cudaStream_t st = (cudaStream_t)stream;
+    if (!scratch) return -3;  // first call on this device made during capture
     const int np = n > 0 ? (int)((n + kChunk - 1) / kChunk) : 1;
     const double scale = (nrow > 1 && ncol > 0) ? 1.0 / ((double)(nrow - 1) * ncol) : 0.0;
     mse_chunk_kernel<<<np, 256, 0, st>>>(trace_dev, target_dev, dLdv_dev, scratch, n, ncol, scale);
+    if (cudaGetLastError() != cudaSuccess) return -3;
     mse_chunk_final_kernel<<<1, 256, 0, st>>>(scratch, np, loss_dev, scale);
     return cudaGetLastError() == cudaSuccess ? 0 : -3;
 }

@@ -992,6 +992,12 @@ int hx_mse_loss_grad_dev(hx_ctx* ctx, const double* trace_dev, const double* tar
     return 0;
 }
 
+int hx_rcp_nz_dev(const double* x_dev, double* y_dev, int n, void* stream) {
+    if ((n > 0 && (!x_dev || !y_dev)) || n < 0) return -1;
+    if (hx::launch_rcp_nz(x_dev, y_dev, n, (cudaStream_t)stream) != cudaSuccess) return -3;
+    return 0;
+}
+
 int hx_last_kernel_ms(hx_ctx* ctx, int which, double* ms, int* launches) {
     if (!ctx || which < 0 || which > 2) return -1;
     if (which == 2) {  // the reverse kernel's launches alone

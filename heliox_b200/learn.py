@@ -23,50 +23,62 @@ from .model import CellGroup
 from .runtime import Sim
 
 
-@dataclass(frozen=True)
-class MethodSpec:
-    name: str
-    precise: bool = True
+try:
+    # The reference's own plugin types, when its package is installed beside
+    # this one: AdjointMethod then satisfies heliox_learn.GradientMethod,
+    # accepts heliox_learn.MappedSignal and returns heliox_learn.ReplayGrads.
+    from heliox_learn.method import GradientMethod, MethodSpec  # type: ignore
+    from heliox_learn.signals import MappedSignal, ReplayGrads  # type: ignore
+
+    REFERENCE_TYPES = True
+except ImportError:
+    # The same types restated (field names, validation and messages of
+    # python_lib/heliox_learn/method.py:7-32 and signals.py:9-37, 94-99) for
+    # hosts without the reference package.
+    REFERENCE_TYPES = False
+
+    @dataclass(frozen=True)
+    class MethodSpec:  # type: ignore[no-redef]
+        name: str
+        precise: bool = True
+
+    @runtime_checkable
+    class GradientMethod(Protocol):  # type: ignore[no-redef]
+        @property
+        def spec(self) -> MethodSpec: ...
+
+        def capture(self, runtime: Any, *, state: Any) -> Any: ...
+
+        def backward(self, runtime: Any, *, captured: Any, dL_dprobe: Any) -> Any: ...
+
+    @dataclass(frozen=True)
+    class MappedSignal:  # type: ignore[no-redef]
+        """Handles gathered and scatter-added into N columns: out[dest[j]] += scale[j] * x[handles[j]]."""
+
+        name: str
+        handles: Sequence[int]
+        dest: np.ndarray  # int32 (len(handles),)
+        scale: np.ndarray  # float32 (len(handles),)
+
+        def __post_init__(self) -> None:
+            if self.dest.ndim != 1 or self.scale.ndim != 1:
+                raise ValueError(f"MappedSignal({self.name}): dest/scale must be 1D arrays")
+            if int(self.dest.shape[0]) != len(self.handles) or int(self.scale.shape[0]) != len(self.handles):
+                raise ValueError(f"MappedSignal({self.name}): size mismatch")
+            if self.dest.dtype != np.int32:
+                raise TypeError(f"MappedSignal({self.name}): dest must be int32 (got {self.dest.dtype})")
+            if self.scale.dtype != np.float32:
+                raise TypeError(f"MappedSignal({self.name}): scale must be float32 (got {self.scale.dtype})")
+
+    @dataclass(frozen=True)
+    class ReplayGrads:  # type: ignore[no-redef]
+        dw_out_n: np.ndarray  # float32 (N,)
+        dx_lr_it: Optional[np.ndarray] = None
 
 
-@runtime_checkable
-class GradientMethod(Protocol):
-    @property
-    def spec(self) -> MethodSpec: ...
-
-    def capture(self, runtime: Any, *, state: Any) -> Any: ...
-
-    def backward(self, runtime: Any, *, captured: Any, dL_dprobe: Any) -> Any: ...
-
-
-@dataclass(frozen=True)
-class MappedSignal:
-    """Handles gathered and scatter-added into N columns: out[dest[j]] += scale[j] * x[handles[j]]."""
-
-    name: str
-    handles: Sequence[int]
-    dest: np.ndarray  # int32 (len(handles),)
-    scale: np.ndarray  # float32 (len(handles),)
-
-    def __post_init__(self) -> None:
-        if self.dest.ndim != 1 or self.scale.ndim != 1:
-            raise ValueError(f"MappedSignal({self.name}): dest/scale must be 1D arrays")
-        if int(self.dest.shape[0]) != len(self.handles) or int(self.scale.shape[0]) != len(self.handles):
-            raise ValueError(f"MappedSignal({self.name}): size mismatch")
-        if self.dest.dtype != np.int32:
-            raise TypeError(f"MappedSignal({self.name}): dest must be int32 (got {self.dest.dtype})")
-        if self.scale.dtype != np.float32:
-            raise TypeError(f"MappedSignal({self.name}): scale must be float32 (got {self.scale.dtype})")
-
-    @property
-    def n_columns(self) -> int:
-        return int(self.dest.max()) + 1 if self.dest.size else 0
-
-
-@dataclass(frozen=True)
-class ReplayGrads:
-    dw_out_n: np.ndarray  # float32 (N,)
-    dx_lr_it: Optional[np.ndarray] = None
+def n_columns(p: MappedSignal) -> int:
+    """Columns N of a mapping: 1 + the largest destination column."""
+    return int(p.dest.max()) + 1 if p.dest.size else 0
 
 
 @dataclass(frozen=True)
@@ -143,7 +155,7 @@ class AdjointMethod:
             raise ValueError("AdjointMethod.backward needs the state with the parameter mapping")
         runtime.sim.backward(np.asarray(dL_dprobe, dtype=np.float64), keys=())
         p = state.params
-        dw = runtime.sim.reduce_grads_f32(list(p.handles), p.dest, p.scale, p.n_columns)
+        dw = runtime.sim.reduce_grads_f32(list(p.handles), p.dest, p.scale, n_columns(p))
         return ReplayGrads(dw_out_n=dw, dx_lr_it=None)
 
 

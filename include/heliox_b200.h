@@ -483,13 +483,25 @@ int hx_mse_loss_grad_dev(hx_ctx* ctx, const double* trace_dev, const double* tar
  * the process exits), so nrow*ncol may be at most 4,096 * 65,536 = 2^28
  * elements; larger inputs return -2 (with a message on stderr) and do no work.
  * Work is enqueued on `stream` (NULL = the legacy default stream) of the
- * current device.  The first call on a device resolves the scratch array's
- * device address; make that first call before any stream capture.  All calls
- * on a device share the array: calls that overlap on the GPU race.  Returns 0,
- * -1 bad argument, -2 size beyond the maximum, -3 CUDA error.  It has no
- * counterpart in the reference. */
+ * current device.  Every call made outside stream capture resolves the
+ * scratch array's device address (so a cudaDeviceReset in between is
+ * harmless); a call during capture reuses the last one, so make the first
+ * call on a device before any stream capture.  All calls on a device share
+ * the array: calls that overlap on the GPU race.  Returns 0, -1 bad argument,
+ * -2 size beyond the maximum, -3 CUDA error of this call's launches, -4 an
+ * earlier CUDA error is pending (left for the caller, no work done).  It has
+ * no counterpart in the reference. */
 int hx_mse_loss_grad_noalloc(const double* trace_dev, const double* target_dev, int nrow, int ncol, double* dLdv_dev,
                              double* loss_dev, void* stream);
+
+/* ---- verification -------------------------------------------------------------- */
+/* y[i] = the reciprocal the step kernels use in place of IEEE division in the
+ * mechanism rate functions (hardware estimate + two Newton-Raphson steps), for
+ * device arrays of n doubles on the current device; work on `stream`.  Its
+ * domain is normal |x| whose reciprocal is normal (about 2^-1022 .. 2^1022);
+ * subnormal inputs flush to zero.  Returns 0, -1 bad argument, -3 CUDA error.
+ * No reference counterpart (the reference divides). */
+int hx_rcp_nz_dev(const double* x_dev, double* y_dev, int n, void* stream);
 
 /* ---- timing (CUDA events on the launch stream) ---------------------------------- */
 /* Milliseconds of the last forward-capture / backward kernel work, measured with

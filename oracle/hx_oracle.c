@@ -46,12 +46,24 @@ static double vtrap(double x, double y) {
     if (fabs(x / y) < 1e-6) return y * (1 - x / y / 2);
     return x / (exp(x / y) - 1);
 }
-/* d vtrap / dx, derivative of the branch vtrap() takes */
+/* d vtrap / dx, derivative of the branch vtrap() takes.  Near the removable
+ * singularity (1e-6 <= |u| < 0.05, u = x/y) the numerator exp(u) - 1 - u exp(u)
+ * is taken from its series -sum_{n>=2} (n-1) u^n / n! and the denominator from
+ * expm1: the direct difference loses ~1e-16/u^2 of it to cancellation. */
 static double dvtrap(double x, double y) {
-    if (fabs(x / y) < 1e-6) return -0.5;
-    double e = exp(x / y);
+    double u = x / y;
+    if (fabs(u) < 1e-6) return -0.5;
+    if (fabs(u) < 0.05) {
+        static const double c[10] = {1.0 / 2, 2.0 / 6, 3.0 / 24, 4.0 / 120, 5.0 / 720, 6.0 / 5040,
+                                     7.0 / 40320, 8.0 / 362880, 9.0 / 3628800, 10.0 / 39916800};
+        double t = c[9];
+        for (int n = 8; n >= 0; n--) t = t * u + c[n];
+        double em1 = expm1(u);
+        return -(u * u) * t / (em1 * em1);
+    }
+    double e = exp(u);
     double em1 = e - 1;
-    return (em1 - (x / y) * e) / (em1 * em1);
+    return (em1 - u * e) / (em1 * em1);
 }
 
 typedef struct {

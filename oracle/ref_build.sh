@@ -6,8 +6,9 @@
 # (oracle/ref_harness.cpp) are ours.  Flags follow the reference's
 # CMakeLists.txt:7-31 (C++20, -ffp-contract=off, -fno-fast-math).
 set -euo pipefail
-REF=${HX_REFERENCE:-/root/reference}/src
 HERE=$(cd "$(dirname "$0")" && pwd)
+# the reference checkout: HX_REFERENCE, else the one beside this repository
+REF=${HX_REFERENCE:-$HERE/../../reference}/src
 OUT=$HERE/_ref
 OBJ=$OUT/obj
 mkdir -p "$OBJ"

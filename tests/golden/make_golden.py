@@ -3,7 +3,7 @@
 Needs the reference sources (to build oracle/_ref/hxref_run with
 oracle/ref_build.sh); run from the repository root:
 
-    python tests/golden/make_golden.py [case ...]
+    python tests/golden/make_golden.py [case ...]   (case or case_perm3)
 
 Each case exports a seeded synthetic group in CoreNEURON format
 (heliox_b200.coredat), runs the reference (read_coredat -> data_format_trans ->
@@ -50,6 +50,12 @@ def _lib_mixed():
     return g
 
 
+# cases also run with the reference's node permutation type 3 (its default in
+# python_lib/heliox_learn/runtime.py:13: the branch split of
+# permute_order.cpp:641-1170 solved by cpu_solve_permute3, simulate.cpp:631-713),
+# stored as <case>_perm3.npz
+PERM3 = ("ball_and_stick", "trees3", "tree_deep", "net_spiking", "lib_cells")
+
 ADAM = dict(n=64, steps=25, lr=1e-3, inv_record_steps=0.25, beta1=0.9, beta2=0.999, eps=1e-8, impedance=2.0, seed=5)
 
 
@@ -73,16 +79,21 @@ def main(names=None):
     print("adam", ws.shape)
     for name in CASES:
         make_case(name)
+    for name in PERM3:
+        make_case(name, permute_type=3)
 
 
-def make_case(name):
+def make_case(name, permute_type=0):
+    if name.endswith("_perm3"):
+        name, permute_type = name[: -len("_perm3")], 3
     make, nstep, probes = CASES[name]
     g = make()
     p = np.asarray(probes if probes is not None else list(g.soma_nodes()) + [g.nnode - 1], dtype=np.int32)
-    tr, spk = O.ref_forward(g, nstep, probe=p)
-    np.savez_compressed(os.path.join(HERE, f"{name}.npz"), trace=tr, probes=p, nstep=nstep,
+    tr, spk = O.ref_forward(g, nstep, probe=p, permute_type=permute_type)
+    out = f"{name}_perm{permute_type}.npz" if permute_type else f"{name}.npz"
+    np.savez_compressed(os.path.join(HERE, out), trace=tr, probes=p, nstep=nstep, permute_type=permute_type,
                         spikes=np.asarray(spk, dtype=np.float64).reshape(-1, 2))
-    print(name, tr.shape, len(spk))
+    print(out, tr.shape, len(spk))
 
 
 if __name__ == "__main__":

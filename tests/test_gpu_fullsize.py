@@ -1,0 +1,229 @@
+"""GPU parity at the benchmark configurations' own sizes and horizons.
+
+* config 2: the exact group bench.py times (1024 seeded cells, 4000 steps,
+  one wave of 148 CTAs), forward and backward with the soma-MSE gradient
+  against the teacher; 32 cells spread over the batch (every 32nd, plus the
+  largest and the smallest) are checked against per-cell oracle runs;
+* config 3: the 50,000-compartment cell split across CTAs, 2000 steps,
+  gradients of every segment's conductances;
+* config 4: a network of the config-4 recipe (its own 16 cells, 100 Exp2Syn
+  each plus a NetStim) over the full 8000-step horizon;
+* config 5: three epochs of the Adam fit of the coupled 302-cell network (900
+  HalfGap pairs, 2000 graded synapses, 8000 steps), each epoch against the
+  oracle's forward and adjoint at the device's parameters and the reference's
+  Adam restated (oracle.adam_port).
+
+Tolerances (north_star): voltages within 1e-9 of the trace scale, gradients
+within 1e-7 of the largest oracle gradient of their kind (norm-wise bounds),
+spike lists equal with times within dt.  Each test also prints the largest
+per-element relative error over the elements above 1e-3 of the kind's scale,
+and bounds it loosely (a per-element bound on near-zero gradients measures
+cancellation, not parity).
+
+The oracle runs on the host cores of the GPU box, in spawned worker processes.
+"""
+import multiprocessing as mp
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+SEED0 = 20240  # bench.py's config-2 seed
+
+
+def _errs(got, ref):
+    """(norm-wise relative error, largest per-element relative error above 1e-3 of the scale)."""
+    got = np.asarray(got, dtype=np.float64)
+    ref = np.asarray(ref, dtype=np.float64)
+    scale = float(np.max(np.abs(ref))) if ref.size else 0.0
+    if scale == 0.0:
+        return float(np.max(np.abs(got))) if got.size else 0.0, 0.0
+    norm = float(np.max(np.abs(got - ref))) / scale
+    big = np.abs(ref) >= 1e-3 * scale
+    elem = float(np.max(np.abs(got[big] - ref[big]) / np.abs(ref[big]))) if big.any() else 0.0
+    return norm, elem
+
+
+def _cell_job(args):
+    c, T, dcol = args
+    from heliox_b200 import synth
+    from oracle import oracle as O
+
+    g = synth.random_tree_cell(SEED0 + c)
+    tr, gr = O.adjoint(g, T, dcol)
+    return c, tr[:, 0], {k: gr[k] for k in ("hh.gnabar", "hh.gkbar", "hh.gl", "pas.g", "cm")}
+
+
+def test_config2_bench_group_full_horizon():
+    import torch
+
+    from heliox_b200 import synth
+    from heliox_b200.runtime import Sim
+
+    T = 4000
+    g = synth.random_tree_batch(1024, seed0=SEED0)
+    teacher = synth.perturb_conductances(g, 0.2, seed=SEED0 + 7)
+    s = Sim(0)
+    s.load_group(teacher)
+    target = s.simulate(T)
+    s.close()
+    s = Sim(0)
+    s.load_group(g)
+    st = s.plan_stats()
+    assert st["npack"] == torch.cuda.get_device_properties(0).multi_processor_count  # one wave, as benched
+    tr = s.forward_capture(T)
+    dl = np.zeros_like(tr)
+    dl[1:] = 2.0 * (tr[1:] - target[1:]) / (T * g.ncell)
+    keys = ("hh.gnabar", "hh.gkbar", "hh.gl", "pas.g", "cm")
+    gr = s.backward(dl, keys=keys)
+    s.close()
+    sizes = np.bincount(g.cell_of_node(), minlength=g.ncell)
+    pick = sorted(set(range(0, g.ncell, 32)) | {int(np.argmax(sizes)), int(np.argmin(sizes))})
+    cell = g.cell_of_node()
+    with mp.get_context("spawn").Pool(min(len(pick), mp.cpu_count() or 1)) as pool:
+        res = pool.map(_cell_job, [(c, T, np.ascontiguousarray(dl[:, c:c + 1])) for c in pick])
+    worst = {"v": (0.0, 0.0)}
+    for c, vref, gref in res:
+        ev = _errs(tr[:, c], vref)
+        assert ev[0] <= 1e-9, (c, ev)
+        worst["v"] = max(worst["v"], ev)
+        for k in keys:
+            tab = {"hh": g.hh, "pas": g.pas}.get(k.split(".")[0])
+            idx = np.nonzero(cell == c)[0] if k == "cm" else np.nonzero(cell[tab.nodes] == c)[0]
+            e = _errs(gr[k][idx], gref[k])
+            assert e[0] <= 1e-7, (c, k, e)
+            assert e[1] <= 1e-4, (c, k, e)
+            worst[k] = max(worst.get(k, (0.0, 0.0)), e)
+    print("config 2 (norm-wise, per-element) worst over", len(pick), "cells:", worst)
+
+
+def test_config3_giant_cell_full_horizon():
+    from heliox_b200 import synth
+    from heliox_b200.runtime import Sim
+    from oracle import oracle as O
+
+    T = 2000
+    g = synth.giant_cell()
+    probes = np.unique(np.linspace(0, g.nnode - 1, 64).astype(np.int32))
+    s = Sim(0)
+    s.load_group(g)
+    assert s.plan_stats()["nsub"] > 0  # split across CTAs, as benched
+    tr = s.forward_capture(T, probes=probes)
+    dl = np.random.default_rng(3).standard_normal(tr.shape) * 1e-3
+    keys = ("hh.gnabar", "hh.gkbar", "hh.gl", "pas.g")
+    gr = s.backward(dl, keys=keys)
+    s.close()
+    ref, gref = O.adjoint(g, T, dl, probe=probes)
+    ev = _errs(tr, ref)
+    assert ev[0] <= 1e-9, ev
+    out = {"v": ev}
+    for k in keys:
+        e = _errs(gr[k], gref[k])
+        assert e[0] <= 1e-7, (k, e)
+        assert e[1] <= 1e-4, (k, e)
+        out[k] = e
+    print("config 3 (norm-wise, per-element):", out)
+
+
+def test_config4_recipe_network_full_horizon():
+    from heliox_b200 import synth
+    from heliox_b200.runtime import Sim
+    from oracle import oracle as O
+
+    T = 8000
+    g = synth.network_config4_shard(16, 0, 1)
+    s = Sim(0)
+    s.load_group(g)
+    tr = s.forward_capture(T)
+    dl = np.random.default_rng(4).standard_normal(tr.shape) * 1e-3
+    keys = ("Exp2Syn.weight", "Exp2Syn.e", "hh.gnabar", "pas.g")
+    gr = s.backward(dl, keys=keys)
+    gid, t = s.spikes()
+    s.close()
+    ref, gref = O.adjoint(g, T, dl)
+    ev = _errs(tr, ref)
+    assert ev[0] <= 1e-9, ev
+    want = sorted((int(b), float(a)) for a, b in gref["spikes"])
+    got = sorted(zip(gid.tolist(), t.tolist()))
+    assert len(got) == len(want) and len(want) > 0
+    assert all(a[0] == b[0] and abs(a[1] - b[1]) <= g.dt for a, b in zip(got, want))
+    out = {"v": ev, "spikes": len(want)}
+    for k in keys:
+        e = _errs(gr[k], gref[k])
+        assert e[0] <= 1e-7, (k, e)
+        assert e[1] <= 1e-4, (k, e)
+        out[k] = e
+    print("config 4 recipe, 16 cells x 8000 steps (norm-wise, per-element):", out)
+
+
+def test_config5_adam_fit_matches_oracle():
+    """Config 5's fit on the device, epoch by epoch against the oracle at the
+    same parameters: the loss and the gradient the device Adam receives (read
+    from the optimizer's slot buffer) against the oracle's forward and adjoint
+    at the device's current parameters, and the device's update against the
+    reference's Adam restated (oracle.adam_port) over the device's gradient
+    history.  (Chaining the oracle's own updates instead would compare two
+    trajectories of a fit whose first Adam step moves the 1e-4..1e-3 uS
+    couplings by about their own size.)"""
+    import torch
+
+    from heliox_b200 import synth
+    from heliox_b200.learn import mse_objective
+    from heliox_b200.runtime import Sim
+    from heliox_b200.shard import _wrap
+    from oracle import oracle as O
+    import ctypes as C
+
+    T, lr, epochs = 8000, 1e-3, 3
+    g = synth.worm_config5()
+    teacher = g.copy()
+    rng = np.random.default_rng(SEED0 + 5)
+    teacher.halfgap.fields["g"] = teacher.halfgap.fields["g"] * np.exp(0.2 * rng.standard_normal(g.halfgap.n))
+    teacher.graded.fields["w"] = teacher.graded.fields["w"] * np.exp(0.2 * rng.standard_normal(g.graded.n))
+    s = Sim(0)
+    s.load_group(teacher)
+    target = s.simulate(T)
+    s.close()
+    keys = ("HalfGap.g", "neuron_to_neuron_syn_lr.w")
+    nh = g.halfgap.n
+    s = Sim(0)
+    s.load_group(g)
+    h = [s.get_variable_handle("HalfGap", "g", i) for i in range(nh)] + \
+        [s.get_variable_handle("neuron_to_neuron_syn_lr", "w", i) for i in range(g.graded.n)]
+    opt = s.create_optimizer("adam")
+    s.optimizer_add_external_grads(opt, h, impedance=1.0)
+    w0 = np.concatenate([s.get_param_array(k) for k in keys])
+    hist, worst = [], {"loss": 0.0, "grad": (0.0, 0.0), "adam": 0.0}
+    for ep in range(epochs):
+        cur = g.copy()
+        p = np.concatenate([s.get_param_array(k) for k in keys])
+        cur.halfgap.fields["g"] = p[:nh].copy()
+        cur.graded.fields["w"] = p[nh:].copy()
+        tr = s.forward_capture(T)
+        loss, dl = mse_objective(tr, target)
+        s.backward(dl, keys=())
+        s.optimizer_grads_from_backward(opt)
+        ptr, n = s.optimizer_grad_buffer(opt)
+        torch.cuda.synchronize()
+        gdev = _wrap(ptr, n, C.c_double, "cuda").cpu().numpy().copy()
+        s.optimizer_step_with_inv_record_steps(opt, lr, 1.0)
+        hist.append(gdev)
+        # the oracle at the same parameters
+        tr_ref, _ = O.forward(cur, T)
+        loss_ref, dl_ref = mse_objective(tr_ref, target)
+        _, gr = O.adjoint(cur, T, dl_ref)
+        gref = np.concatenate([gr["HalfGap.g"], gr["neuron_to_neuron_syn_lr.w"]])
+        assert abs(loss - loss_ref) <= 1e-9 * abs(loss_ref), (ep, loss, loss_ref)
+        eg = _errs(gdev, gref)
+        assert eg[0] <= 1e-7, (ep, eg)
+        # the device update: the reference's Adam over the device's gradient history
+        ws, _, _ = O.adam_port(w0, np.array(hist), lr, 1.0)
+        wdev = np.concatenate([s.get_param_array(k) for k in keys])
+        ea = float(np.max(np.abs(wdev - ws[-1])))
+        assert ea <= 1e-15 * max(1.0, float(np.max(np.abs(ws[-1])))), (ep, ea)
+        worst["loss"] = max(worst["loss"], abs(loss - loss_ref) / abs(loss_ref))
+        worst["grad"] = max(worst["grad"], eg)
+        worst["adam"] = max(worst["adam"], ea)
+    s.close()
+    print("config 5 Adam,", epochs, "epochs: worst loss / gradient (norm-wise, per-element) / update errors:", worst)
