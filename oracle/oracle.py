@@ -149,6 +149,55 @@ def ref_forward(g, nstep: int, probe: Optional[Sequence[int]] = None, v_init: Op
         shutil.rmtree(tmp, ignore_errors=True)
 
 
+REF_GPU = os.path.join(_HERE, "_ref", "hxref_run_gpu")
+
+
+def ref_forward_gpu(g, nstep: int, probe: Optional[Sequence[int]] = None, v_init: Optional[float] = None,
+                    timing_only: bool = False, permute_type: int = 0):
+    """Run the reference's GPU integrator (Simulate(GPU): fadvance_gpu and its
+    kernels, oracle/_ref/hxref_run_gpu) on ``g`` with node permutation
+    ``permute_type`` (0: cuda_solve_matrix, 3: its cop_solve_kernel); needs a
+    CUDA device.
+
+    Returns (trace, spikes, seconds): with ``timing_only`` the trace holds only
+    the initial and final rows and the seconds are the fadvance loop between
+    two device synchronisations; otherwise every step is recorded (a copy of
+    v back to the host per step) and the seconds include those copies.
+    """
+    import shutil
+    import tempfile
+
+    from heliox_b200.coredat import write_coredat
+
+    if not os.path.exists(REF_GPU):
+        raise RuntimeError("reference GPU harness not built (oracle/ref_build.sh)")
+    probe = np.ascontiguousarray(g.soma_nodes() if probe is None else probe, dtype=np.int32)
+    tmp = tempfile.mkdtemp(prefix="hxrefg_")
+    try:
+        data = os.path.join(tmp, "data")
+        write_coredat(g, data)
+        pf = os.path.join(tmp, "probes.i32")
+        probe.tofile(pf)
+        tf = os.path.join(tmp, "trace.f64")
+        spk = os.path.join(tmp, "spk")
+        vi = float(g.v_init if v_init is None else v_init)
+        r = subprocess.run([REF_GPU, data, str(int(permute_type)), repr(float(g.dt)), str(int(nstep)), repr(vi), pf,
+                            tf, spk, "gpu-time" if timing_only else "gpu"], capture_output=True, text=True)
+        if r.returncode != 0:
+            raise RuntimeError(f"reference GPU run failed ({r.returncode}):\n{r.stdout[-2000:]}\n{r.stderr[-2000:]}")
+        trace = np.fromfile(tf, dtype=np.float64).reshape(nstep + 1, probe.shape[0])
+        spikes = []
+        sf = os.path.join(spk, "spk.dat")
+        if os.path.exists(sf):
+            for line in open(sf):
+                t, gid = line.split()
+                spikes.append((float(t), int(gid)))
+        secs = [float(x.split()[1]) for x in r.stdout.splitlines() if x.startswith("HXREF_FADVANCE_S")]
+        return trace, spikes, secs[-1]
+    finally:
+        shutil.rmtree(tmp, ignore_errors=True)
+
+
 def adam_port(w0, grads, lr, inv_record_steps, beta1=0.9, beta2=0.999, eps=1e-8, impedance=1.0):
     """Restatement of AdamOptimizer::step_cpu (src/optimizer/optimizer.cpp:351-397)
     for one weight per entry, same operation order.  Returns (weights after each

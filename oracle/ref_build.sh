@@ -60,4 +60,7 @@ g++ $CXXFLAGS -I/usr/local/cuda/include -c "$HERE/ref_nodev.cpp" -o "$OBJ/_nodev
 # shared CUDA runtime, so that the host-only definitions in _nodev.o take precedence
 nvcc -gencode arch=compute_100a,code=sm_100a -o "$OUT/hxref_run" "$OBJ"/*.o -cudart shared -lpthread \
   -Xlinker -rpath=/usr/local/cuda/lib64
-echo "built $OUT/hxref_run"
+# the same integrator against the real CUDA runtime: the reference's GPU path
+nvcc -gencode arch=compute_100a,code=sm_100a -o "$OUT/hxref_run_gpu" $(ls "$OBJ"/*.o | grep -v '/_nodev.o$') \
+  -cudart shared -lpthread -Xlinker -rpath=/usr/local/cuda/lib64
+echo "built $OUT/hxref_run $OUT/hxref_run_gpu"

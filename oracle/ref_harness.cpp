@@ -20,10 +20,20 @@
 // reference's integration alone, without loading or output) is printed as
 // "HXREF_FADVANCE_S <seconds>".
 //
+//   hxref_run_gpu <same arguments> gpu|gpu-time
+// (the binary linked against the real CUDA runtime, oracle/_ref/hxref_run_gpu)
+// runs the reference's GPU integrator instead (Simulate(GPU): fadvance_gpu,
+// src/simulate.cu:722-771, its mechanism kernels and cuda_solve_matrix):
+// "gpu" copies the voltages back after every step to record the probes;
+// "gpu-time" records only the initial and final states and times the fadvance
+// loop between two device synchronisations (HXREF_FADVANCE_S).
+//
 //   hxref_run --adam <n> <steps> <lr> <inv_record_steps> <beta1> <beta2> <eps> <impedance> <in.f64> <out.f64>
 // runs the reference's AdamOptimizer (src/optimizer/optimizer.cpp) on the CPU:
 // in.f64 holds n initial weights followed by steps x n gradients; out.f64
 // receives the weights after every step (steps x n) and the final m and v.
+#include <cuda_runtime_api.h>
+
 #include <chrono>
 #include <cstdio>
 #include <cstdlib>
@@ -81,10 +91,18 @@ static int run_adam(int argc, char** argv) {
 
 int main(int argc, char** argv) {
     if (argc > 1 && std::string(argv[1]) == "--adam") return run_adam(argc, argv);
-    if (argc != 9) {
-        std::fprintf(stderr, "usage: %s dir permute_type dt nstep v_init probes.i32 trace.f64 spike_dir\n", argv[0]);
+    if (argc != 9 && argc != 10) {
+        std::fprintf(stderr, "usage: %s dir permute_type dt nstep v_init probes.i32 trace.f64 spike_dir [gpu|gpu-time]\n",
+                     argv[0]);
         return 2;
     }
+    const std::string gmode = argc == 10 ? argv[9] : "";
+    if (!gmode.empty() && gmode != "gpu" && gmode != "gpu-time") {
+        std::fprintf(stderr, "mode must be gpu or gpu-time\n");
+        return 2;
+    }
+    const Mode mode = gmode.empty() ? CPU : GPU;
+    const bool every_step = gmode != "gpu-time";
     const std::string dir = argv[1];
     const int ptype = std::atoi(argv[2]);
     const double dt = std::atof(argv[3]);
@@ -106,11 +124,11 @@ int main(int argc, char** argv) {
     std::unique_ptr<coreneuron::CoreData*[]> arr;
     const std::string files = dir + "/files.dat";
     int ngroup = read_coredat(arr, dir.c_str(), files.c_str(), 0, false, 1000);
-    Simulate* sim = new Simulate(CPU, BufferEnable::NONE);
+    Simulate* sim = new Simulate(mode, BufferEnable::NONE);
     sim->dt = dt;
     sim->tstop = nstep * dt;
     sim->output_folder = argv[8];
-    data_format_trans(sim->neuron_group_list, arr, ngroup, CPU, sim->dt);
+    data_format_trans(sim->neuron_group_list, arr, ngroup, mode, sim->dt);
     for (int i = 0; i < ngroup; i++) delete arr[i];
     sim->permute_type = ptype;
     // HalfGap: vgap of instance i follows the voltage of a source node, wired
@@ -142,15 +160,30 @@ int main(int argc, char** argv) {
         for (int& q : probes) q = g->permute[q];
     std::vector<double> trace((size_t)(nstep + 1) * probes.size());
     auto record = [&](int row) {
+        if (mode == GPU) g->vecdata_v->update_cpu_data_from_gpu();
         const double* v = g->vecdata_v->get_cpu_data();
         for (size_t q = 0; q < probes.size(); q++) trace[(size_t)row * probes.size() + q] = v[probes[q]];
     };
     record(0);
+    auto t1 = t0;
+    if (mode == GPU && !every_step) {
+        cudaDeviceSynchronize();
+        t1 = std::chrono::steady_clock::now();  // gpu-time: the fadvance loop alone
+    }
     for (int k = 0; k < nstep; k++) {
         sim->fadvance();
-        record(k + 1);
+        if (every_step) record(k + 1);
     }
-    const double secs = std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
+    if (mode == GPU) cudaDeviceSynchronize();
+    const double secs = std::chrono::duration<double>(std::chrono::steady_clock::now() - t1).count();
+    if (!every_step) record(nstep);
+    if (mode == GPU) {
+        const cudaError_t e = cudaGetLastError();
+        if (e != cudaSuccess) {
+            std::fprintf(stderr, "CUDA error: %s\n", cudaGetErrorString(e));
+            return 5;
+        }
+    }
     std::printf("HXREF_FADVANCE_S %.9f\n", secs);
     std::fflush(stdout);
     sim->output_spikes();
