@@ -203,7 +203,7 @@ SIGNATURES = {
     "hx_set_exchange": (C.c_int, [C.c_void_p, EXCHANGE_FN, C.c_void_p, C.c_int, C.c_int]),
     "hx_set_window": (C.c_int, [C.c_void_p, C.c_int]),
     "hx_get_window": (C.c_int, [C.c_void_p, _ip]),
-    "hx_exchange_merge_status": (C.c_int, [_ip, C.c_int, _ip, _ip, _ip]),
+    "hx_exchange_merge_status": (C.c_int, [_ip, C.c_int, _ip, _ip, _ip, _ip]),
 }
 
 _LIB = None

@@ -151,6 +151,8 @@ struct hx_ctx {
     DevBuf<int2> st_send, st_recv;  // per-rank status pair after the last window
     DevBuf<int> win_n, log_n;
     int win_cap = 0, log_cap = 0, win_cap_user = 0;
+    int win_cap_cur = 0;    // agreed window buffer size of a multi-rank exchange (grows on overflow)
+    DevBuf<int> win_max;    // largest window spike count of the current forward
     // NetStim trains of the last forward length (host generator, routed each forward)
     std::vector<double> ns_interval, ns_number, ns_start, ns_noise;
     int ns_rng = 0, ns_steps = -1, ns_count = 0;

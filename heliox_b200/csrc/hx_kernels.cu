@@ -849,9 +849,12 @@ __global__ void route_kernel(const int2* __restrict__ spk, const int* __restrict
 
 // appends the window's spikes to the forward's spike log
 __global__ void log_append_kernel(const int2* __restrict__ win, const int* __restrict__ win_n, int win_cap,
-                                  int2* log, int* log_n, int log_cap, int* err) {
+                                  int2* log, int* log_n, int log_cap, int* err, int* win_max) {
     const int n = min(*win_n, win_cap);
-    if (*win_n > win_cap && threadIdx.x == 0 && blockIdx.x == 0) atomicOr(err, 4);
+    if (threadIdx.x == 0 && blockIdx.x == 0) {
+        if (*win_n > win_cap) atomicOr(err, 4);
+        atomicMax(win_max, *win_n);
+    }
     const int base = *log_n;
     for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x)
         if (base + i < log_cap) log[base + i] = win[i];
@@ -862,9 +865,10 @@ __global__ void log_advance_kernel(const int* __restrict__ win_n, int win_cap, i
 }
 
 // A rank's status after its last window: (error bits | extra, largest bucket
-// count over the nstep steps).  One block; the ranks all-gather it.
-__global__ void net_status_kernel(const int* __restrict__ err, const int* __restrict__ ev_cnt, int nstep, int extra,
-                                  int2* out) {
+// count over the nstep buckets), (largest window spike count, 0).  One block;
+// the ranks all-gather it.
+__global__ void net_status_kernel(const int* __restrict__ err, const int* __restrict__ ev_cnt, int nstep,
+                                  const int* __restrict__ win_max, int extra, int2* out) {
     __shared__ int red[256];
     int m = 0;
     for (int k = threadIdx.x; k < nstep; k += blockDim.x) m = max(m, ev_cnt[k]);
@@ -874,7 +878,10 @@ __global__ void net_status_kernel(const int* __restrict__ err, const int* __rest
         if ((int)threadIdx.x < s) red[threadIdx.x] = max(red[threadIdx.x], red[threadIdx.x + s]);
         __syncthreads();
     }
-    if (threadIdx.x == 0) *out = make_int2(*err | extra, red[0]);
+    if (threadIdx.x == 0) {
+        out[0] = make_int2(*err | extra, red[0]);
+        out[1] = make_int2(*win_max, 0);
+    }
 }
 
 // The library's reciprocal over an array (verification of rcp_nz against IEEE division)
@@ -889,8 +896,9 @@ cudaError_t launch_rcp_nz(const double* x, double* y, int n, cudaStream_t st) {
     return cudaGetLastError();
 }
 
-cudaError_t launch_net_status(const int* err, const int* ev_cnt, int nstep, int extra, int2* out, cudaStream_t st) {
-    net_status_kernel<<<1, 256, 0, st>>>(err, ev_cnt, nstep, extra, out);
+cudaError_t launch_net_status(const int* err, const int* ev_cnt, int nstep, const int* win_max, int extra, int2* out,
+                              cudaStream_t st) {
+    net_status_kernel<<<1, 256, 0, st>>>(err, ev_cnt, nstep, win_max, extra, out);
     return cudaGetLastError();
 }
 
@@ -924,11 +932,11 @@ cudaError_t launch_route(const int2* spk, const int* nspk_dev, int nspk_max, con
 }
 
 cudaError_t launch_log_append(const int2* win, const int* win_n, int win_cap, int2* log, int* log_n, int log_cap,
-                              int* err, cudaStream_t st) {
+                              int* err, int* win_max, cudaStream_t st) {
     int blocks = (win_cap + 255) / 256;
     if (blocks > 148) blocks = 148;
     if (blocks < 1) blocks = 1;
-    log_append_kernel<<<blocks, 256, 0, st>>>(win, win_n, win_cap, log, log_n, log_cap, err);
+    log_append_kernel<<<blocks, 256, 0, st>>>(win, win_n, win_cap, log, log_n, log_cap, err, win_max);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return e;
     log_advance_kernel<<<1, 1, 0, st>>>(win_n, win_cap, log_n);

@@ -41,9 +41,10 @@ cudaError_t launch_route(const int2* spk, const int* nspk_dev, int nspk_max, con
                          const int* syn_pack, int npack, int* ev_cnt, int* ev_syn, int ev_cap, int* err,
                          cudaStream_t st);
 cudaError_t launch_log_append(const int2* win, const int* win_n, int win_cap, int2* log, int* log_n, int log_cap,
-                              int* err, cudaStream_t st);
+                              int* err, int* win_max, cudaStream_t st);
 cudaError_t launch_rcp_nz(const double* x, double* y, int n, cudaStream_t st);
-cudaError_t launch_net_status(const int* err, const int* ev_cnt, int nstep, int extra, int2* out, cudaStream_t st);
+cudaError_t launch_net_status(const int* err, const int* ev_cnt, int nstep, const int* win_max, int extra, int2* out,
+                              cudaStream_t st);
 cudaError_t launch_gather(const double* src, const int* idx, double* dst, int n, cudaStream_t st);
 cudaError_t launch_scatter(const double* src, const int* idx, double* dst, int n, cudaStream_t st);
 constexpr int kMsePartials = 256;

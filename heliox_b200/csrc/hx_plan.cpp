@@ -352,6 +352,31 @@ std::string build_plan(const hx_group_desc& g, int nodes_per_warp, int max_pack_
                 bin_n[b] += usize[c];
                 if ((int)bins[b].size() < kW) room.insert({(long long)cap - bin_n[b], b});
             }
+            // repair: a cell left over goes into a CTA whose room a move of one
+            // of its cells to another CTA (with room for that cell) makes enough
+            std::vector<int> still;
+            for (int c : left) {
+                bool placed = false;
+                for (size_t bi = nbase; bi < bins.size() && !placed; bi++) {
+                    const int free_i = cap - bin_n[bi];
+                    if ((int)bins[bi].size() > kW) continue;
+                    for (size_t yi = 0; yi < bins[bi].size() && !placed; yi++) {
+                        const int y = bins[bi][yi];
+                        if (free_i + usize[y] < usize[c]) continue;
+                        for (size_t bj = nbase; bj < bins.size(); bj++) {
+                            if (bj == bi || cap - bin_n[bj] < usize[y] || (int)bins[bj].size() >= kW) continue;
+                            bins[bj].push_back(y);
+                            bin_n[bj] += usize[y];
+                            bins[bi][yi] = c;
+                            bin_n[bi] += usize[c] - usize[y];
+                            placed = true;
+                            break;
+                        }
+                    }
+                }
+                if (!placed) still.push_back(c);
+            }
+            left.swap(still);
             if (left.empty()) break;
             if (K >= (long long)order.size()) {  // one cell per CTA already: keep the rest in CTAs of their own
                 for (int c : left) {
@@ -361,16 +386,8 @@ std::string build_plan(const hx_group_desc& g, int nodes_per_warp, int max_pack_
                 break;
             }
         }
-        // drop bins left empty (fewer units than CTAs)
-        std::vector<std::vector<int>> kept;
-        std::vector<int> kept_n;
-        for (size_t k = 0; k < bins.size(); k++)
-            if (!bins[k].empty()) {
-                kept.push_back(std::move(bins[k]));
-                kept_n.push_back(bin_n[k]);
-            }
-        bins.swap(kept);
-        bin_n.swap(kept_n);
+        // bins left empty stay for the balancing below to fill; the ones still
+        // empty after it are dropped there
     } else {
         for (int c : order) {
             int b = -1;

@@ -280,9 +280,9 @@ int hx_load_group(hx_ctx* ctx, const hx_group_desc* desc) {
     // topology tables and the per-segment arrays (network groups keep their
     // synapse states in global memory).  A single cell larger than that is
     // split across CTAs, whose kernels keep 10 doubles per node.  The plan is
-    // checked against the exact table sizes and rebuilt with a capacity 1.5 %
-    // smaller while it does not fit: the step kernels are latency bound, so
-    // the nodes a wave of CTAs holds sets the throughput.
+    // checked against the exact table sizes and rebuilt with a capacity
+    // smaller by its overshoot while it does not fit: the step kernels are
+    // latency bound, so the nodes a wave of CTAs holds sets the throughput.
     int optin = 0, nsm = 0;
     HXC(cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, ctx->device));
     HXC(cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, ctx->device));
@@ -296,7 +296,7 @@ int hx_load_group(hx_ctx* ctx, const hx_group_desc* desc) {
     const int warps = split_kernels ? hx::kSplitThreads / 32 : hx::kWarpsPerCta;
     std::string e = hx::build_plan(*desc, ctx->pack_target, cap_nodes, ctx->P, nsm, warps);
     if (!e.empty()) return fail(ctx, "invalid group: " + e);
-    for (int shrink = 0; shrink < 60 && desc->nnode > 0; shrink++) {
+    for (int shrink = 0; shrink < 200 && desc->nnode > 0; shrink++) {
         const hx::Plan& Pc = ctx->P;
         hx::DevGroup Gt{};
         Gt.smem_n = std::max(Pc.max_pack_nodes, 1);
@@ -307,7 +307,9 @@ int hx_load_group(hx_ctx* ctx, const hx_group_desc* desc) {
         const size_t need = split_kernels ? std::max(hx::split_fwd_smem_bytes(Gt), hx::split_bwd_smem_bytes(Gt))
                                           : std::max(hx::fwd_smem_bytes(Gt), hx::bwd_smem_bytes(Gt));
         if (need <= (size_t)optin) break;
-        cap_nodes = (int)(cap_nodes * 0.985);
+        // shrink by the overshoot (at least 0.2 %, at most 1.5 % a step)
+        const double f = std::max(0.985, std::min(0.998, 0.999 * (double)optin / (double)need));
+        cap_nodes = std::min(cap_nodes - 1, (int)(cap_nodes * f));
         e = hx::build_plan(*desc, ctx->pack_target, cap_nodes, ctx->P, nsm, warps);
         if (!e.empty()) return fail(ctx, "invalid group: " + e);
     }

@@ -427,18 +427,18 @@ int hx_net_forward(hx_ctx* ctx, int nstep, double v_init, double* trace_dev, boo
     // exchange buffers, or whose exchange itself fails, returns at once (the
     // process group's timeout then ends the peers' collective).
     const bool multi = ctx->exchange && ctx->nranks > 1;
+    // window spike buffer: one rank alone holds its bound (a PreSyn fires at
+    // most every other step); ranks that exchange send buffers of the agreed
+    // size win_cap_cur (most windows carry far fewer spikes than the bound),
+    // grown on every rank alike when one overflows
     const int own_cap = ncell * ((W + 1) / 2) + 1;
     const size_t nbucket = (size_t)std::max(nstep, 1) * (size_t)std::max(P.npack, 1);  // (step, pack) event buckets
-    ctx->win_cap = ctx->win_cap_user > 0 ? ctx->win_cap_user : own_cap;
-    HXC(ctx->win_send.ensure(ctx->win_cap));
-    HXC(ctx->win_recv.ensure((size_t)ctx->win_cap * std::max(ctx->nranks, 1)));
     if (multi) {
-        HXC(ctx->st_send.ensure(1));
-        HXC(ctx->st_recv.ensure((size_t)ctx->nranks));
+        HXC(ctx->st_send.ensure(2));
+        HXC(ctx->st_recv.ensure(2 * (size_t)ctx->nranks));
     }
+    HXC(ctx->win_max.ensure(1));
     auto setup = [&]() -> int {
-        if (ctx->win_cap < own_cap)  // all ranks must exchange buffers of one size
-            return hx_fail(ctx, "exchange capacity below this group's bound of " + std::to_string(own_cap));
         if (net_netstim(ctx, nstep)) return -1;
         if (capture && net_plan_tape(ctx, nstep, W)) return -1;
         ctx->log_cap = (int)std::min<long long>((long long)ncell * std::max(64, nstep / 20 + 1), 1LL << 26);
@@ -453,6 +453,9 @@ int hx_net_forward(hx_ctx* ctx, int nstep, double v_init, double* trace_dev, boo
     hx::DevProbe PV = hx_probe_view(ctx);
     const double half_dt = ctx->dt / 2;
     for (int attempt = 0; attempt < 6; attempt++) {
+        ctx->win_cap = multi ? ctx->win_cap_cur : own_cap;
+        HXC(ctx->win_send.ensure(ctx->win_cap));
+        HXC(ctx->win_recv.ensure((size_t)ctx->win_cap * std::max(ctx->nranks, 1)));
         if (ok && ctx->ev_syn.ensure(nbucket * ctx->ev_cap) != cudaSuccess) {
             hx_fail(ctx, "event bucket allocation failed");
             if (!multi) return -1;
@@ -462,6 +465,7 @@ int hx_net_forward(hx_ctx* ctx, int nstep, double v_init, double* trace_dev, boo
         auto init_attempt = [&]() -> int {
             HXC(cudaMemsetAsync(ctx->ev_cnt.p, 0, nbucket * 4, st));
             HXC(cudaMemsetAsync(ctx->dev_err.p, 0, 4, st));
+            HXC(cudaMemsetAsync(ctx->win_max.p, 0, 4, st));
             HXC(cudaMemsetAsync(ctx->log_n.p, 0, 4, st));
             HXC(cudaMemsetAsync(ctx->cs_ps_flag.p, 0, (size_t)std::max(ncell, 1) * 4, st));
             double* v0 = ctx->coupled ? ctx->vbuf.p : ctx->sv.p;
@@ -505,7 +509,7 @@ int hx_net_forward(hx_ctx* ctx, int nstep, double v_init, double* trace_dev, boo
             hx::DevState S{vin, ctx->sm.p, ctx->sh.p, ctx->sn.p};
             HXC(hx::launch_fwd(ctx->G, S, T, write_tape, PV, trace_dev, ctx->tmid.p, k0, k1, st, &N));
             HXC(hx::launch_log_append(ctx->win_send.p, ctx->win_n.p, ctx->win_cap, ctx->spk_log.p, ctx->log_n.p,
-                                      ctx->log_cap, ctx->dev_err.p, st));
+                                      ctx->log_cap, ctx->dev_err.p, ctx->win_max.p, st));
             launches += 2;
             return 0;
         };
@@ -545,25 +549,26 @@ int hx_net_forward(hx_ctx* ctx, int nstep, double v_init, double* trace_dev, boo
             HXC(cudaMemcpyAsync(ctx->sv.p, ctx->vbuf.p + (size_t)(nstep & 1) * nn, nn * 8, cudaMemcpyDeviceToDevice,
                                 st));
         }
-        int err = 0, need = 0, bad_rank = -1;
+        int err = 0, need = 0, win_need = 0, bad_rank = -1;
         if (multi) {
-            // every rank's (error bits, largest bucket count) after its last window
-            if (ok && hx::launch_net_status(ctx->dev_err.p, ctx->ev_cnt.p, (int)nbucket, 0, ctx->st_send.p, st) !=
-                          cudaSuccess) {
+            // every rank's (error bits, largest bucket count, largest window) after its last window
+            if (ok && hx::launch_net_status(ctx->dev_err.p, ctx->ev_cnt.p, (int)nbucket, ctx->win_max.p, 0,
+                                            ctx->st_send.p, st) != cudaSuccess) {
                 ok = false;
                 local_err = "status kernel launch failed";
             }
             if (!ok) {  // a stopped rank reports only that it stopped
-                const int2 ab = make_int2(HX_XS_ABORT, 0);
-                cudaMemcpyAsync(ctx->st_send.p, &ab, sizeof(int2), cudaMemcpyHostToDevice, st);
+                const int2 ab[2] = {make_int2(HX_XS_ABORT, 0), make_int2(0, 0)};
+                cudaMemcpyAsync(ctx->st_send.p, ab, sizeof(ab), cudaMemcpyHostToDevice, st);
             }
-            if (ctx->exchange(ctx->exchange_user, ctx->st_send.p, ctx->st_recv.p, 1, (void*)st) != 0)
+            if (ctx->exchange(ctx->exchange_user, ctx->st_send.p, ctx->st_recv.p, 2, (void*)st) != 0)
                 return hx_fail(ctx, "spike exchange callback failed (status)");
-            std::vector<int2> all(ctx->nranks);
+            std::vector<int2> all(2 * (size_t)ctx->nranks);
             HXC(cudaMemcpyAsync(all.data(), ctx->st_recv.p, all.size() * sizeof(int2), cudaMemcpyDeviceToHost, st));
             HXC(cudaEventRecord(ctx->ev[1], st));
             HXC(cudaStreamSynchronize(st));
-            hx_exchange_merge_status(reinterpret_cast<const int*>(all.data()), ctx->nranks, &err, &need, &bad_rank);
+            hx_exchange_merge_status(reinterpret_cast<const int*>(all.data()), ctx->nranks, &err, &need, &win_need,
+                                     &bad_rank);
             if (err & HX_XS_ABORT)
                 return hx_fail(ctx, local_err.empty()
                                         ? "rank " + std::to_string(bad_rank) + " failed in the multi-rank forward"
@@ -576,7 +581,11 @@ int hx_net_forward(hx_ctx* ctx, int nstep, double v_init, double* trace_dev, boo
         ctx->launches[0] = launches + (multi ? 1 : 0);
         if (err & HX_XS_LATE_EVENT)
             return hx_fail(ctx, "an event fell inside a simulated window (window longer than the delay)");
-        if (err & HX_XS_WINDOW) return hx_fail(ctx, "window spike buffer overflow");
+        if (err & HX_XS_WINDOW) {
+            if (!multi) return hx_fail(ctx, "window spike buffer overflow");
+            // the largest window over all ranks, so every rank grows alike
+            ctx->win_cap_cur = std::max(ctx->win_cap_cur * 2, win_need + win_need / 4 + 8);
+        }
         if (err & HX_XS_BUCKET) {
             if (!multi) {
                 std::vector<int> cnt(nbucket);
@@ -585,13 +594,14 @@ int hx_net_forward(hx_ctx* ctx, int nstep, double v_init, double* trace_dev, boo
             }
             // every rank takes the same (largest) need, so all rerun alike
             ctx->ev_cap = std::max(ctx->ev_cap * 2, need + need / 4 + 8);
-            continue;  // the run depended on dropped events: run it again with room for all
         }
+        if (err & (HX_XS_BUCKET | HX_XS_WINDOW))
+            continue;  // the run depended on dropped events or spikes: run it again with room for all
         ctx->captured = capture;
         ctx->nstep = nstep;
         return 0;
     }
-    return hx_fail(ctx, "event buckets kept overflowing");
+    return hx_fail(ctx, "event buckets or window buffers kept overflowing");
 }
 
 // ---------------------------------------------------------------- backward
@@ -753,22 +763,26 @@ int hx_set_exchange(hx_ctx* ctx, hx_exchange_fn exchange, void* user, int nranks
     ctx->exchange_user = user;
     ctx->nranks = exchange ? nranks : 1;
     ctx->win_cap_user = exchange ? cap_entries : 0;
+    ctx->win_cap_cur = exchange ? (cap_entries > 0 ? cap_entries : 1024) : 0;
     ctx->ev_cap = 0;
     return 0;
 }
 
-int hx_exchange_merge_status(const int* status, int nranks, int* flags, int* need, int* first_rank) {
-    if (!status || nranks < 1 || !flags || !need || !first_rank) return -1;
-    int f = 0, nd = 0, hard = -1, soft = -1;
+int hx_exchange_merge_status(const int* status, int nranks, int* flags, int* need, int* win_need, int* first_rank) {
+    if (!status || nranks < 1 || !flags || !need || !win_need || !first_rank) return -1;
+    int f = 0, nd = 0, wn = 0, hard = -1, soft = -1;
     for (int r = 0; r < nranks; r++) {
-        const int b = status[2 * r], q = status[2 * r + 1];
+        const int* q = status + 4 * r;
+        const int b = q[0];
         f |= b;
-        nd = std::max(nd, q);
-        if ((b & ~HX_XS_BUCKET) && hard < 0) hard = r;
-        if ((b & HX_XS_BUCKET) && soft < 0) soft = r;
+        nd = std::max(nd, q[1]);
+        wn = std::max(wn, q[2]);
+        if ((b & ~(HX_XS_BUCKET | HX_XS_WINDOW)) && hard < 0) hard = r;
+        if ((b & (HX_XS_BUCKET | HX_XS_WINDOW)) && soft < 0) soft = r;
     }
     *flags = f;
     *need = nd;
+    *win_need = wn;
     *first_rank = hard >= 0 ? hard : soft;
     return 0;
 }

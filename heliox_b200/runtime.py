@@ -172,7 +172,8 @@ class Sim:
         """Install the multi-GPU spike exchange: ``fn(send_ptr, recv_ptr, cap_entries, stream_ptr)``
         must all-gather ``cap_entries`` (gid, step) int pairs per rank from
         ``send_ptr`` into ``recv_ptr`` on the given stream (``None`` removes it).
-        ``cap_entries`` must be the same on every rank (``shard.exchange_capacity``)."""
+        ``cap_entries`` is the initial window buffer size, the same on every
+        rank (0: the library's default; it grows on overflow)."""
         if fn is None:
             self._xfn = None
             self._check(self._L.hx_set_exchange(self._ctx, _lib.EXCHANGE_FN(), None, 1, 0), "hx_set_exchange")

@@ -118,8 +118,10 @@ def window_of(g: CellGroup) -> int:
 
 
 def exchange_capacity(g: CellGroup, nranks: int, window: int) -> int:
-    """Window spike buffer size shared by all ranks: the largest shard's cells
-    times ceil(window/2) (a PreSyn fires at most every other step) plus one."""
+    """The bound on one window's spikes of the largest shard: its cells times
+    ceil(window/2) (a PreSyn fires at most every other step) plus one.  A
+    window buffer this large never overflows; ``Sim.set_exchange`` may start
+    far smaller (0: the library's default), growing on overflow."""
     most = max(c1 - c0 for c0, c1 in cell_ranges(g, nranks))
     return most * ((window + 1) // 2) + 1
 
@@ -163,8 +165,8 @@ def allgather_exchange(group=None, device: str = "cuda"):
 
     The library hands over its window send buffer and a receive buffer of
     nranks times its size (``cap`` (gid, step) int32 pairs per rank; ``cap`` is
-    1 for the status pair after the last window) and its launch stream; the
-    hook wraps the buffers without copying and all-gathers on that stream.
+    2 for the status after the last window) and its launch stream; the hook
+    wraps the buffers without copying and all-gathers on that stream.
     ``device="cpu"`` takes host buffers (gloo tests of the protocol).
     """
     import ctypes as C
@@ -198,19 +200,21 @@ def allreduce_sum(group=None, device: str = "cuda"):
     return fn
 
 
-def merge_status(status: np.ndarray) -> Tuple[int, int, int]:
-    """(flags, need, first_rank) of the gathered per-rank status pairs, by the
-    library's own rule (``hx_exchange_merge_status``; host only)."""
+def merge_status(status: np.ndarray) -> Tuple[int, int, int, int]:
+    """(flags, bucket need, window need, first_rank) of the gathered per-rank
+    status (4 ints per rank), by the library's own rule
+    (``hx_exchange_merge_status``; host only)."""
     import ctypes as C
 
     from . import _lib
 
     L = _lib.load()
     st = np.ascontiguousarray(status, dtype=np.int32).reshape(-1)
-    f, nd, r = C.c_int(0), C.c_int(0), C.c_int(0)
-    if L.hx_exchange_merge_status(_lib.iptr(st), st.shape[0] // 2, C.byref(f), C.byref(nd), C.byref(r)) != 0:
+    f, nd, wn, r = C.c_int(0), C.c_int(0), C.c_int(0), C.c_int(0)
+    if L.hx_exchange_merge_status(_lib.iptr(st), st.shape[0] // 4, C.byref(f), C.byref(nd), C.byref(wn),
+                                  C.byref(r)) != 0:
         raise ValueError("bad status array")
-    return int(f.value), int(nd.value), int(r.value)
+    return int(f.value), int(nd.value), int(wn.value), int(r.value)
 
 
 def pad_spikes(gid: np.ndarray, step: np.ndarray, cap: int) -> np.ndarray:

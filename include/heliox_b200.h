@@ -20,7 +20,7 @@
 extern "C" {
 #endif
 
-#define HX_ABI_VERSION 6
+#define HX_ABI_VERSION 7
 
 typedef struct hx_ctx hx_ctx;
 
@@ -370,29 +370,33 @@ int hx_get_spikes(hx_ctx* ctx, int cap, int* gid, double* t, int* n);
  * the reference's NetStim (src/spike/netstim.cpp:207-330). */
 int hx_netstim_trains(const hx_group_desc* desc, int nstep, int cap, int* id, int* step, int* n);
 typedef int (*hx_exchange_fn)(void* user, const void* send_dev, void* recv_dev, int cap_entries, void* stream);
-/* cap_entries: the window buffer size, identical on every rank and at least
- * (this group's cells) * ceil(window / 2) (a PreSyn fires at most every other
- * step); pass the maximum over ranks.  0 = this group's own bound (one rank).
- * The hook is called once per window with cap_entries and, after the last
- * window, once more with cap_entries = 1: every rank's status pair
- * (HX_XS_* bits, largest event-bucket count) is all-gathered, so that all
+/* cap_entries: the window buffer size every rank starts with (identical on
+ * every rank; 0 = 1024 entries).  Most windows carry far fewer spikes than
+ * the bound (cells) * ceil(window / 2) (a PreSyn fires at most every other
+ * step), so the buffer stays small; a window that overflows it on any rank
+ * makes every rank rerun the forward with the agreed larger size, which is
+ * kept for later forwards.  The hook is called once per window with the
+ * current cap_entries and, after the last window, once more with
+ * cap_entries = 2: every rank's status -- (HX_XS_* bits, largest event-bucket
+ * count), (largest window spike count, 0) -- is all-gathered, so that all
  * ranks return the same outcome (a rank whose host work failed keeps
- * exchanging empty windows until then and reports HX_XS_ABORT; a bucket
- * overflow on any rank reruns the forward on every rank).  A hook that
+ * exchanging empty windows until then and reports HX_XS_ABORT; a bucket or
+ * window overflow on any rank reruns the forward on every rank).  A hook that
  * returns nonzero ends the forward on that rank at once; its peers' next
  * collective then ends by the process group's timeout. */
 int hx_set_exchange(hx_ctx* ctx, hx_exchange_fn exchange, void* user, int nranks, int cap_entries);
 /* Status bits of a rank after the last window of a multi-rank forward. */
 #define HX_XS_LATE_EVENT 1 /* an event fell inside an already simulated window */
 #define HX_XS_BUCKET 2     /* a per-step event bucket overflowed (the forward is rerun) */
-#define HX_XS_WINDOW 4     /* the window spike buffer overflowed */
+#define HX_XS_WINDOW 4     /* the window spike buffer overflowed (the forward is rerun) */
 #define HX_XS_ABORT 8      /* the rank's host work failed; it only kept exchanging */
-/* Merge of the gathered status pairs (status[2 r] bits, status[2 r + 1]
- * bucket need of rank r): *flags = OR of the bits, *need = the largest need,
- * *first_rank = the lowest rank with a bit other than HX_XS_BUCKET set (else
- * the lowest with HX_XS_BUCKET, else -1).  Host only; the rule every rank
- * applies, exposed for hosts that drive their own exchange. */
-int hx_exchange_merge_status(const int* status, int nranks, int* flags, int* need, int* first_rank);
+/* Merge of the gathered status (4 ints per rank r: status[4 r] bits,
+ * status[4 r + 1] bucket need, status[4 r + 2] window need, status[4 r + 3]
+ * unused): *flags = OR of the bits, *need and *win_need = the largest needs,
+ * *first_rank = the lowest rank with a bit other than the overflow bits set
+ * (else the lowest with an overflow bit, else -1).  Host only; the rule every
+ * rank applies, exposed for hosts that drive their own exchange. */
+int hx_exchange_merge_status(const int* status, int nranks, int* flags, int* need, int* win_need, int* first_rank);
 /* Steps per forward window of an event network (0 = derived from the smallest
  * NetCon delay of this group); returns the effective value with hx_get_window. */
 int hx_set_window(hx_ctx* ctx, int steps);

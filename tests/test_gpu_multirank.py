@@ -5,7 +5,8 @@ fewer than two GPUs; NVLS is off, the multi-rank tests use plain NCCL).
   oracle run of the whole network -- traces, spikes and weight gradients --
   both for a partition of a given network (shard.shard) and for the config-4
   network built per rank (synth.network_config4_shard, the bench's strong
-  scaling layout, window agreed over the ranks);
+  scaling layout, window agreed over the ranks, a window buffer started far
+  too small so that every rank grows it and reruns together);
 * a host-side failure on one rank (injected into its status pair) makes every
   rank's forward return the error, with no rank left waiting, and the next
   forward runs normally;
@@ -87,7 +88,7 @@ def _worker(rank, world, port, q, mode):
             part = synth.network_config4_shard(12, rank, world)
             base, nsrc = part.meta["gid_base"], part.meta["nsrc_cells"]
             W = _agreed_window(dist, shard.window_of(part))
-            cap = -(-12 // world) * ((W + 1) // 2) + 1
+            cap = 2  # far below the window's spikes: the ranks grow it together and rerun
             ncell_all = 12
         else:
             g = _net()
@@ -102,7 +103,7 @@ def _worker(rank, world, port, q, mode):
             import ctypes as C
 
             def failing(send, recv, cap_, stream):
-                if cap_ == 1 and rank == 1:  # rank 1 reports a failed host step in its status pair
+                if cap_ == 2 and rank == 1:  # rank 1 reports a failed host step in its status
                     t = shard._wrap(send, 2, C.c_int, "cuda")
                     with shard._on_stream(stream, "cuda"):
                         t[0:1].bitwise_or_(8)

@@ -118,21 +118,22 @@ XS_LATE, XS_BUCKET, XS_WINDOW, XS_ABORT = 1, 2, 4, 8
 
 
 def _status_worker(rank, world, port, q):
-    """After the last window every rank all-gathers its (bits, bucket need)
-    pair and applies the library's merge rule.  Scenario 1 injects a host
-    failure on rank 1 (it reports HX_XS_ABORT, as the library does for a rank
-    that stopped launching work) while rank 0's buckets overflowed; scenario
-    2 has only bucket overflows of different sizes."""
+    """After the last window every rank all-gathers its status -- (bits,
+    bucket need), (window need, 0) -- and applies the library's merge rule.
+    Scenario 1 injects a host failure on rank 1 (it reports HX_XS_ABORT, as
+    the library does for a rank that stopped launching work) while rank 0's
+    buckets overflowed; scenario 2 has only overflows of different sizes."""
     import ctypes as C
 
     dist = _init(rank, world, port)
     try:
         fn = shard.allgather_exchange(device="cpu")
         out = []
-        for mine in ({0: (XS_BUCKET, 40), 1: (XS_ABORT, 0)}, {0: (XS_BUCKET, 40), 1: (XS_BUCKET, 90)}):
+        for mine in ({0: (XS_BUCKET, 40, 300, 0), 1: (XS_ABORT, 0, 0, 0)},
+                     {0: (XS_BUCKET, 40, 300, 0), 1: (XS_BUCKET | XS_WINDOW, 90, 2500, 0)}):
             send = np.array(mine[rank], np.int32)
-            recv = np.zeros(2 * world, np.int32)
-            fn(send.ctypes.data_as(C.c_void_p).value, recv.ctypes.data_as(C.c_void_p).value, 1, 0)
+            recv = np.zeros(4 * world, np.int32)
+            fn(send.ctypes.data_as(C.c_void_p).value, recv.ctypes.data_as(C.c_void_p).value, 2, 0)
             out.append(shard.merge_status(recv))
         q.put((rank, out))
     finally:
@@ -143,13 +144,13 @@ def test_status_exchange_agrees_on_failure_gloo():
     res = _spawn(_status_worker)
     (_, a), (_, b) = res
     assert a == b  # every rank reaches the same decision
-    assert a[0] == (XS_BUCKET | XS_ABORT, 40, 1)  # fail together, naming rank 1
-    assert a[1] == (XS_BUCKET, 90, 0)  # rerun together with the largest need
+    assert a[0] == (XS_BUCKET | XS_ABORT, 40, 300, 1)  # fail together, naming rank 1
+    assert a[1] == (XS_BUCKET | XS_WINDOW, 90, 2500, 0)  # rerun together with the largest needs
 
 
 def test_merge_status_rule():
-    assert shard.merge_status(np.array([[0, 3], [0, 7]])) == (0, 7, -1)
-    assert shard.merge_status(np.array([[XS_BUCKET, 3], [XS_WINDOW, 0], [XS_LATE, 1]])) == (7, 3, 1)
+    assert shard.merge_status(np.array([[0, 3, 5, 0], [0, 7, 2, 0]])) == (0, 7, 5, -1)
+    assert shard.merge_status(np.array([[XS_BUCKET, 3, 0, 0], [XS_WINDOW, 0, 9, 0], [XS_LATE, 1, 0, 0]])) == (7, 3, 9, 2)
 
 
 def _allreduce_worker(rank, world, port, q):
