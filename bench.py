@@ -48,6 +48,11 @@ T_STEPS = 4000
 NCELL = 1024
 NCELL_NET = 10000
 SEED0 = 20240
+# DRAM bytes per compartment-step of the network reverse kernel, measured by
+# ncu (dram__bytes_read.sum + dram__bytes_write.sum of one bwd_kernel launch
+# over 1250 config-4 cells x 200 steps, / its compartment-steps); scaled to a
+# launch of the timed configuration as roofline.traffic (config 4 only)
+REV_DRAM_BYTES_PER_UNIT_NET = 409.1
 
 
 def _alg_bytes(g):
@@ -466,7 +471,8 @@ def run_ours(args):
                 "peak_source": peak_src,
                 "unit": "GB/s",
                 "frac": achieved / peak,
-                "traffic": None,
+                "traffic": (REV_DRAM_BYTES_PER_UNIT_NET * ncomp * T / max(nrev, 1) if args.config == 4 else None),
+                "traffic_source": "ncu, 1250 config-4 cells x 200 steps, per compartment-step x this launch's",
                 "alg_bytes_per_launch": rb * T / max(nrev, 1),
                 "launches_per_step": nrev,
                 "kernel_ms_per_step": rev_ms,
