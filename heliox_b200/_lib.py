@@ -76,8 +76,9 @@ HX_P = {
     "cca1.gbcca1": 55,
     "egl19.gbegl19": 56,
     "unc2.gbunc2": 57,
+    "gapjunction_noptr.weight": 58,
 }
-HX_P_COUNT = 58
+HX_P_COUNT = 59
 HX_LIB_NTYPE = 42
 
 
@@ -128,6 +129,7 @@ class GroupDesc(C.Structure):
         ("netstim_rng", C.c_int),
         ("nhalfgap", C.c_int), ("hg_node", _ip), ("hg_src", _ip), ("hg_g", _dp),
         ("ngapj", C.c_int), ("gj_node", _ip), ("gj_pre", _ip), ("gj_g", _dp), ("gj_w", _dp),
+        ("ngapnp", C.c_int), ("gn_node", _ip), ("gn_src", _ip), ("gn_weight", _dp),
         ("ngraded", C.c_int), ("gr_node", _ip), ("gr_pre", _ip), ("gr_w", _dp), ("gr_delta", _dp), ("gr_vth", _dp),
         ("lib", C.POINTER(LibDesc)),
     ]
@@ -168,6 +170,7 @@ SIGNATURES = {
     "hx_set_stream": (C.c_int, [C.c_void_p, C.c_void_p]),
     "hx_set_pack_target": (C.c_int, [C.c_void_p, C.c_int]),
     "hx_set_tape_budget": (C.c_int, [C.c_void_p, C.c_size_t]),
+    "hx_set_split_barrier_limit": (C.c_int, [C.c_void_p, C.c_longlong]),
     "hx_load_group": (C.c_int, [C.c_void_p, C.POINTER(GroupDesc)]),
     "hx_get_plan_stats": (C.c_int, [C.c_void_p, C.POINTER(PlanStats)]),
     "hx_plan_check": (C.c_int, [C.POINTER(GroupDesc), C.c_int, C.POINTER(PlanStats), _dp, _dp]),
@@ -296,6 +299,8 @@ class BoundGroup:
         gj = g.gapjunction
         s.ngapj, s.gj_node, s.gj_pre = gj.n, I(gj.nodes), I(gj.ifields["pre"])
         s.gj_g, s.gj_w = D(gj.fields["g"]), D(gj.fields["w"])
+        gn = g.gapnoptr
+        s.ngapnp, s.gn_node, s.gn_src, s.gn_weight = gn.n, I(gn.nodes), I(gn.ifields["src"]), D(gn.fields["weight"])
         gr = g.graded
         s.ngraded, s.gr_node, s.gr_pre = gr.n, I(gr.nodes), I(gr.ifields["pre"])
         s.gr_w, s.gr_delta, s.gr_vth = D(gr.fields["w"]), D(gr.fields["delta"]), D(gr.fields["Vth"])

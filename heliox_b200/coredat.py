@@ -12,7 +12,8 @@ Mechanism data columns follow the offsets the reference reads
 (``var_in_coredata_idx`` of hh_templated.cu:51-65, pas_templated.cu:13-14,
 iclamp_templated.cu:25-27, capac.cpp:29, eion.cuh:81-86, expsyn.cpp:36-72,
 exp2syn_temp.cuh:22-27, netstim.cpp:56-79, HalfGap.cu:43-47,
-gapjunction_lr.cu:47-53, neuron_to_neuron_syn_lr.cu:70-86); the remaining
+gapjunction_lr.cu:47-53, gapjunction_noptr.cu:28-31,
+neuron_to_neuron_syn_lr.cu:70-86); the remaining
 columns of NEURON's layouts are written as zeros.  Ion instances (na_ion, k_ion)
 sit on every hh node and carry the reversal potentials; their ``iontype``
 flags are 0 (fixed reversal potentials, eion.cuh:155-197).  Every cell gets a
@@ -22,10 +23,11 @@ NetStim j gets PreSyn ``ncell + j`` (gid ``ncell + j``).  Point processes carry
 dparams (area node, point-process slot[, POINTER target node]); POINTERs of
 gapjunction_lr / neuron_to_neuron_syn_lr are voltages (empty pointer2type,
 mech_template.cuh:431-455).  One NetCon per ExpSyn / Exp2Syn instance, ExpSyn
-targets first, in instance order.  HalfGap's vgap is not in the files: the
-reference wires it through Simulate::add_gap_source/add_gap_target
-(simulate.cpp:995-1056); ``write_coredat`` writes the (instance, source node)
-pairs to ``halfgap.i32`` for a driver to replay.
+targets first, in instance order.  HalfGap's vgap and gapjunction_noptr's
+vpre are not in the files: the reference wires them through
+Simulate::add_gap_source/add_gap_target (simulate.cpp:995-1056);
+``write_coredat`` writes the (instance, source node) pairs to ``halfgap.i32``
+and ``gapnoptr.i32`` for a driver to replay.
 """
 from __future__ import annotations
 
@@ -53,53 +55,54 @@ MECH_TABLE: List[Tuple[int, str, int, int, int, int, int, float]] = [
     (11, "NetStim", 4, 1, 0, 9, 2, 0.0),
     (12, "HalfGap", 5, 0, 0, 5, 2, 0.0),
     (13, "gapjunction_lr", 6, 0, 0, 7, 3, 0.0),
-    (14, "neuron_to_neuron_syn_lr", 7, 0, 0, 19, 3, 0.0),
+    (14, "gapjunction_noptr", 7, 0, 0, 4, 2, 0.0),
+    (15, "neuron_to_neuron_syn_lr", 8, 0, 0, 19, 3, 0.0),
 ]
 # library mechanisms (written only for groups that carry them): ca_ion and the
 # user-mech channel set; dsize covers the columns var_in_coredata_idx reads
 # (CaDynamics_E2.cu:57-66, CA_HVA.cu, Ca_LVAst.cu, Im.cu, K_Pst.cu, K_Tst.cu,
 # NaTg.cu:62-70, Nap_Et2.cu, SK_E2.cu:58-62, SKv3_1.cu)
 LIB_MECH_TABLE: List[Tuple[int, str, int, int, int, int, int, float]] = [
-    (15, "ca_ion", 0, 0, 1, 5, 1, 2.0),
-    (16, "CaDynamics_E2", 0, 0, 0, 6, 0, 0.0),
-    (17, "Ca_HVA", 0, 0, 0, 15, 0, 0.0),
-    (18, "Ca_LVAst", 0, 0, 0, 10, 0, 0.0),
-    (19, "Im", 0, 0, 0, 9, 0, 0.0),
-    (20, "K_Pst", 0, 0, 0, 10, 0, 0.0),
-    (21, "K_Tst", 0, 0, 0, 10, 0, 0.0),
-    (22, "NaTg", 0, 0, 0, 9, 0, 0.0),
-    (23, "Nap_Et2", 0, 0, 0, 5, 0, 0.0),
-    (24, "SK_E2", 0, 0, 0, 4, 0, 0.0),
-    (25, "SKv3_1", 0, 0, 0, 4, 0, 0.0),
-    (26, "hd_la", 0, 0, 0, 11, 0, 0.0),
-    (27, "km_la", 0, 0, 0, 13, 0, 0.0),
-    (28, "kca_la", 0, 0, 0, 14, 0, 0.0),
-    (29, "it2_la", 0, 0, 0, 16, 0, 0.0),
-    (30, "kdr_la", 0, 0, 0, 8, 0, 0.0),
-    (31, "sca_la", 0, 0, 0, 18, 0, 0.0),
-    (32, "Ca", 0, 0, 0, 14, 0, 0.0),
-    (33, "shl1_lr", 0, 0, 0, 24, 0, 0.0),
-    (34, "kvs1_lr", 0, 0, 0, 20, 0, 0.0),
-    (35, "irk_lr", 0, 0, 0, 16, 0, 0.0),
-    (36, "egl36_lr", 0, 0, 0, 24, 0, 0.0),
-    (37, "shk1_lr", 0, 0, 0, 20, 0, 0.0),
-    (38, "egl2_lr", 0, 0, 0, 16, 0, 0.0),
-    (39, "cca1_lr", 0, 0, 0, 20, 0, 0.0),
-    (40, "egl19_lr", 0, 0, 0, 20, 0, 0.0),
-    (41, "unc2_lr", 0, 0, 0, 20, 0, 0.0),
-    (42, "kcnl_lr", 0, 0, 0, 16, 0, 0.0),
-    (43, "nca_lr", 0, 0, 0, 9, 0, 0.0),
-    (44, "kqt3_lr", 0, 0, 0, 27, 0, 0.0),
-    (45, "cainternm_lr", 0, 0, 0, 6, 0, 0.0),
-    (46, "shl1", 0, 0, 0, 12, 0, 0.0),
-    (47, "kvs1", 0, 0, 0, 9, 0, 0.0),
-    (48, "irk", 0, 0, 0, 6, 0, 0.0),
-    (49, "egl36", 0, 0, 0, 12, 0, 0.0),
-    (50, "shk1", 0, 0, 0, 9, 0, 0.0),
-    (51, "egl2", 0, 0, 0, 6, 0, 0.0),
-    (52, "cca1", 0, 0, 0, 9, 0, 0.0),
-    (53, "egl19", 0, 0, 0, 9, 0, 0.0),
-    (54, "unc2", 0, 0, 0, 9, 0, 0.0),
+    (16, "ca_ion", 0, 0, 1, 5, 1, 2.0),
+    (17, "CaDynamics_E2", 0, 0, 0, 6, 0, 0.0),
+    (18, "Ca_HVA", 0, 0, 0, 15, 0, 0.0),
+    (19, "Ca_LVAst", 0, 0, 0, 10, 0, 0.0),
+    (20, "Im", 0, 0, 0, 9, 0, 0.0),
+    (21, "K_Pst", 0, 0, 0, 10, 0, 0.0),
+    (22, "K_Tst", 0, 0, 0, 10, 0, 0.0),
+    (23, "NaTg", 0, 0, 0, 9, 0, 0.0),
+    (24, "Nap_Et2", 0, 0, 0, 5, 0, 0.0),
+    (25, "SK_E2", 0, 0, 0, 4, 0, 0.0),
+    (26, "SKv3_1", 0, 0, 0, 4, 0, 0.0),
+    (27, "hd_la", 0, 0, 0, 11, 0, 0.0),
+    (28, "km_la", 0, 0, 0, 13, 0, 0.0),
+    (29, "kca_la", 0, 0, 0, 14, 0, 0.0),
+    (30, "it2_la", 0, 0, 0, 16, 0, 0.0),
+    (31, "kdr_la", 0, 0, 0, 8, 0, 0.0),
+    (32, "sca_la", 0, 0, 0, 18, 0, 0.0),
+    (33, "Ca", 0, 0, 0, 14, 0, 0.0),
+    (34, "shl1_lr", 0, 0, 0, 24, 0, 0.0),
+    (35, "kvs1_lr", 0, 0, 0, 20, 0, 0.0),
+    (36, "irk_lr", 0, 0, 0, 16, 0, 0.0),
+    (37, "egl36_lr", 0, 0, 0, 24, 0, 0.0),
+    (38, "shk1_lr", 0, 0, 0, 20, 0, 0.0),
+    (39, "egl2_lr", 0, 0, 0, 16, 0, 0.0),
+    (40, "cca1_lr", 0, 0, 0, 20, 0, 0.0),
+    (41, "egl19_lr", 0, 0, 0, 20, 0, 0.0),
+    (42, "unc2_lr", 0, 0, 0, 20, 0, 0.0),
+    (43, "kcnl_lr", 0, 0, 0, 16, 0, 0.0),
+    (44, "nca_lr", 0, 0, 0, 9, 0, 0.0),
+    (45, "kqt3_lr", 0, 0, 0, 27, 0, 0.0),
+    (46, "cainternm_lr", 0, 0, 0, 6, 0, 0.0),
+    (47, "shl1", 0, 0, 0, 12, 0, 0.0),
+    (48, "kvs1", 0, 0, 0, 9, 0, 0.0),
+    (49, "irk", 0, 0, 0, 6, 0, 0.0),
+    (50, "egl36", 0, 0, 0, 12, 0, 0.0),
+    (51, "shk1", 0, 0, 0, 9, 0, 0.0),
+    (52, "egl2", 0, 0, 0, 6, 0, 0.0),
+    (53, "cca1", 0, 0, 0, 9, 0, 0.0),
+    (54, "egl19", 0, 0, 0, 9, 0, 0.0),
+    (55, "unc2", 0, 0, 0, 9, 0, 0.0),
 ]
 # data column of each library field (its var_in_coredata_idx); SK_E2.zTau is
 # the GLOBAL zTau_SK_E2 of globals.dat (SK_E2.cu:65-66)
@@ -268,6 +271,7 @@ def write_coredat(g: CellGroup, path: str, file_id: int = 0) -> str:
           nodes=np.zeros(0, dtype=np.int32))
     point("HalfGap", g.halfgap, ((0, "g"),))
     point("gapjunction_lr", g.gapjunction, ((0, "g"), (1, "w")), pointer=g.gapjunction.ifields["pre"])
+    point("gapjunction_noptr", g.gapnoptr, ((0, "weight"),))
     point("neuron_to_neuron_syn_lr", g.graded, ((0, "w"), (1, "g"), (2, "delta"), (3, "k"), (4, "Vth"), (5, "erev"),
                                                 (6, "dvpre")), pointer=g.graded.ifields["pre"])
     npnt = npnt[0]
@@ -325,9 +329,9 @@ def write_coredat(g: CellGroup, path: str, file_id: int = 0) -> str:
     w.line(0)  # BBCOREPOINTER count
     w.line(0)  # VecPlayContinuous count
     w.close()
-    if g.halfgap.n:
-        np.column_stack([np.arange(g.halfgap.n), g.halfgap.ifields["src"]]).astype(np.int32).tofile(
-            os.path.join(path, "halfgap.i32"))
+    for tab, fname in ((g.halfgap, "halfgap.i32"), (g.gapnoptr, "gapnoptr.i32")):
+        if tab.n:
+            np.column_stack([np.arange(tab.n), tab.ifields["src"]]).astype(np.int32).tofile(os.path.join(path, fname))
     return path
 
 
@@ -366,17 +370,18 @@ def read_coredat(path: str, file_id=None) -> CellGroup:
     reads it (read_filesdat, read_mech, global_vars, read_phase1,
     read_phase2; src/io/read_coredat.cpp:258-1120): the node arrays, the
     capacitance, pas, na_ion / k_ion, hh, IClamp, ExpSyn, Exp2Syn, NetStim,
-    HalfGap, gapjunction_lr and neuron_to_neuron_syn_lr instances, the
+    HalfGap, gapjunction_lr, gapjunction_noptr and neuron_to_neuron_syn_lr instances, the
     library mechanisms (ca_ion, CaDynamics_E2 and the user-mech channel set),
     the PreSyns and one NetCon per ExpSyn / Exp2Syn instance.  HalfGap sources
-    come from ``halfgap.i32`` when present.  A file with other mechanisms, more
+    and gapjunction_noptr sources come from ``halfgap.i32`` / ``gapnoptr.i32``
+    when present.  A file with other mechanisms, more
     than one NetCon on a synapse instance, per-node initial voltages or
     playback vectors is rejected with a ValueError naming what is not
     supported.  ``file_id``: the group to read (default: the only one listed in
     files.dat).
     """
     from .model import MechTable, _f64, _i32, empty_table, EXPSYN_FIELDS, EXP2SYN_FIELDS, NETSTIM_FIELDS, \
-        HALFGAP_FIELDS, GAPJ_FIELDS, GRADED_FIELDS
+        HALFGAP_FIELDS, GAPJ_FIELDS, GAPNP_FIELDS, GRADED_FIELDS
 
     with open(os.path.join(path, "files.dat")) as f:
         toks = f.read().split()
@@ -497,6 +502,7 @@ def read_coredat(path: str, file_id=None) -> CellGroup:
     halfgap = tab("HalfGap", ((0, "g"),), HALFGAP_FIELDS, ("src",))
     gapj = tab("gapjunction_lr", ((0, "g"), (1, "w")), GAPJ_FIELDS, ("pre",),
                lambda pd: {"pre": _i32(pd[:, 2])})
+    gapnp = tab("gapjunction_noptr", ((0, "weight"),), GAPNP_FIELDS, ("src",))
     graded = tab("neuron_to_neuron_syn_lr", ((0, "w"), (1, "g"), (2, "delta"), (3, "k"), (4, "Vth"), (5, "erev"),
                                              (6, "dvpre")), GRADED_FIELDS, ("pre",),
                  lambda pd: {"pre": _i32(pd[:, 2])})
@@ -539,16 +545,17 @@ def read_coredat(path: str, file_id=None) -> CellGroup:
     for name, s in seen.items():
         if not s.all():
             raise ValueError("a synapse instance without a NetCon is not supported")
-    hg_path = os.path.join(path, "halfgap.i32")
-    if halfgap.n and os.path.exists(hg_path):
-        pairs = np.fromfile(hg_path, dtype=np.int32).reshape(-1, 2)
-        halfgap.ifields["src"][pairs[:, 0]] = pairs[:, 1]
+    for tb, fname in ((halfgap, "halfgap.i32"), (gapnp, "gapnoptr.i32")):
+        wpath = os.path.join(path, fname)
+        if tb.n and os.path.exists(wpath):
+            pairs = np.fromfile(wpath, dtype=np.int32).reshape(-1, 2)
+            tb.ifields["src"][pairs[:, 0]] = pairs[:, 1]
     lib = _read_lib(tabs, glob)
     g = CellGroup(ncell=int(ncell), parent=_i32(parent), a=_f64(a), b=_f64(b), area=_f64(area), cm=_f64(cm),
                   hh=hh, pas=pas, iclamp=iclamp, celsius=glob.get("celsius", 6.3), dt=glob.get("dt", 0.025),
                   v_init=float(v[0]) if n else -65.0, name=os.path.basename(os.path.normpath(path)),
                   expsyn=expsyn, exp2syn=exp2syn, netstim=netstim, halfgap=halfgap, gapjunction=gapj,
-                  graded=graded, ps_thresh=_f64(ps_thresh), lib=lib)
+                  gapnoptr=gapnp, graded=graded, ps_thresh=_f64(ps_thresh), lib=lib)
     g.validate()
     return g
 

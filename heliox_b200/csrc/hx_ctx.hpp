@@ -81,6 +81,7 @@ struct hx_ctx {
     std::string err;
     int pack_target = 0;
     size_t tape_budget = 0;
+    long long split_spin_limit = hx::kSplitSpinLimitDefault;
     bool loaded = false;
     hx::Plan P;
     double dt = 0.025, celsius = 6.3;
@@ -130,7 +131,8 @@ struct hx_ctx {
 
     // ---- network (hx_runtime_net.cu)
     bool net = false, coupled = false;
-    int nexp = 0, nexp2 = 0, nsyn = 0, nstim = 0, nhg = 0, ngj = 0, ngr = 0;
+    // ngj: device gap instances (gapjunction_lr ngj_lr, then gapjunction_noptr ngnp)
+    int nexp = 0, nexp2 = 0, nsyn = 0, nstim = 0, nhg = 0, ngj = 0, ngj_lr = 0, ngnp = 0, ngr = 0;
     int gid_base = 0, nsrc_cells = 0, nsrc = 0;
     int window = 0, window_user = 0;
     double dmin = 0.0;

@@ -84,7 +84,10 @@ struct DevSplit {
     double *xvp;                       // v of each root's parent (forward)
     unsigned* bar;
     int* err;
+    // sleeps of ~100 ns a barrier wait takes before it gives up and sets *err
+    long long spin_limit;
 };
+constexpr long long kSplitSpinLimitDefault = 20000000LL;  // ~2 s
 
 // Network parts of a group (step kernels instantiated with kNet = true).
 // Instance arrays are in GPU order: sorted by GPU node, ExpSyn before Exp2Syn

@@ -57,7 +57,9 @@ static size_t kind_count(const hx_ctx* c, int kind) {
             return (size_t)c->nhg;
         case HX_P_GAPJ_G:
         case HX_P_GAPJ_W:
-            return (size_t)c->ngj;
+            return (size_t)c->ngj_lr;
+        case HX_P_GAPNP_W:
+            return (size_t)c->ngnp;
         case HX_P_GRADED_W:
             return (size_t)c->ngr;
     }
@@ -68,7 +70,9 @@ static size_t kind_count(const hx_ctx* c, int kind) {
 
 // Device storage of a kind: node-indexed for density mechanisms and cm, per
 // instance for IClamp and the network kinds.  ExpSyn and Exp2Syn share one
-// array per variable (GPU synapse order), owned by the ExpSyn kind.
+// array per variable (GPU synapse order), owned by the ExpSyn kind;
+// gapjunction_lr and gapjunction_noptr share the gap arrays (noptr instances
+// carry g = weight, w = 1), owned by the gapjunction_lr kinds.
 static size_t kind_store(const hx_ctx* c, int kind) {
     switch (kind) {
         case HX_P_IC_AMP:
@@ -84,6 +88,8 @@ static size_t kind_store(const hx_ctx* c, int kind) {
         case HX_P_GAPJ_G:
         case HX_P_GAPJ_W:
             return (size_t)c->ngj;
+        case HX_P_GAPNP_W:
+            return 0;
         case HX_P_GRADED_W:
             return (size_t)c->ngr;
     }
@@ -93,7 +99,10 @@ static size_t kind_store(const hx_ctx* c, int kind) {
 }
 
 static int store_kind(int kind) {
-    return kind == HX_P_EXP2SYN_W ? HX_P_EXPSYN_W : kind == HX_P_EXP2SYN_E ? HX_P_EXPSYN_E : kind;
+    return kind == HX_P_EXP2SYN_W   ? HX_P_EXPSYN_W
+           : kind == HX_P_EXP2SYN_E ? HX_P_EXPSYN_E
+           : kind == HX_P_GAPNP_W   ? HX_P_GAPJ_G
+                                    : kind;
 }
 double* hx_kind_ptr(hx_ctx* c, int kind) { return c->prm[store_kind(kind)].p; }
 size_t hx_grad_base(const hx_ctx* c, int kind) { return c->grad_off[store_kind(kind)]; }
@@ -185,6 +194,14 @@ int hx_set_pack_target(hx_ctx* ctx, int nodes_per_warp) {
 int hx_set_tape_budget(hx_ctx* ctx, size_t bytes) {
     if (!ctx) return -1;
     ctx->tape_budget = bytes;
+    return 0;
+}
+
+int hx_set_split_barrier_limit(hx_ctx* ctx, long long sleeps) {
+    if (!ctx) return -1;
+    if (sleeps < 0) return fail(ctx, "split barrier limit must be >= 0");
+    ctx->split_spin_limit = sleeps ? sleeps : hx::kSplitSpinLimitDefault;
+    ctx->X.spin_limit = ctx->split_spin_limit;
     return 0;
 }
 
@@ -424,7 +441,9 @@ int hx_load_group(hx_ctx* ctx, const hx_group_desc* desc) {
     for (int k = 0; k < HX_P_COUNT; k++) ctx->grad_off[k + 1] = ctx->grad_off[k] + kind_store(ctx, k);
     HXC(ctx->grad.ensure(ctx->grad_off[HX_P_COUNT]));
     for (int k = 0; k < hx::kLibKinds; k++) ctx->L.grad[k] = ctx->grad.p + ctx->grad_off[HX_P_CADYN_GAMMA + k];
-    HXC(ctx->stage_dev.ensure(ctx->grad_off[HX_P_COUNT] + std::max(nn, (size_t)ctx->nsyn)));
+    // staging of per-kind gathers at grad_off[k]: kinds without storage of their
+    // own (Exp2Syn, gapjunction_noptr) stage past their offset
+    HXC(ctx->stage_dev.ensure(ctx->grad_off[HX_P_COUNT] + std::max({nn, (size_t)ctx->nsyn, (size_t)ctx->ngj})));
 
     hx::DevGroup& G = ctx->G;
     G = hx::DevGroup{};
@@ -519,6 +538,7 @@ int hx_load_group(hx_ctx* ctx, const hx_group_desc* desc) {
         X.xvp = ctx->xvp.p;
         X.bar = ctx->split_bar.p;
         X.err = ctx->split_err.p;
+        X.spin_limit = ctx->split_spin_limit;
     }
     {
         std::vector<double*> ptrs(HX_P_COUNT);

@@ -115,9 +115,13 @@ int ions_needed(int t) {
 
 }  // namespace
 
+// one past the last library kind (the kinds after it are network kinds again)
+static constexpr int kLibKindEnd = HX_P_UNC2_G + 1;
+static_assert(kLibKindEnd - HX_P_CADYN_GAMMA == hx::kLibKinds, "library kinds");
+
 int hx_lib_type_of_kind(int kind) {
     if (kind >= HX_P_CADYN_GAMMA && kind <= HX_P_CADYN_MINCAI) return HX_LIB_CADYN;
-    if (kind >= HX_P_CA_HVA_G && kind < HX_P_COUNT) return kind - HX_P_CA_HVA_G + HX_LIB_CA_HVA;
+    if (kind >= HX_P_CA_HVA_G && kind < kLibKindEnd) return kind - HX_P_CA_HVA_G + HX_LIB_CA_HVA;
     return -1;
 }
 
@@ -139,7 +143,7 @@ int hx_lib_load(hx_ctx* ctx, const hx_group_desc* desc) {
         }
     cudaStream_t st = ctx->st;
     if (!any) {
-        for (int k = HX_P_CADYN_GAMMA; k < HX_P_COUNT; k++) {
+        for (int k = HX_P_CADYN_GAMMA; k < kLibKindEnd; k++) {
             ctx->kmap_h[k].assign(1, 0);
             HXC(ctx->kmap[k].upload(ctx->kmap_h[k], st));
             HXC(ctx->prm[k].ensure(1));
@@ -185,7 +189,7 @@ int hx_lib_load(hx_ctx* ctx, const hx_group_desc* desc) {
     std::vector<int> inst(HX_LIB_NTYPE, 0);
     std::vector<std::vector<double>> prm(hx::kLibKinds);
     for (int k = 0; k < hx::kLibKinds; k++) prm[k].assign(1, 0.0);
-    for (int k = HX_P_CADYN_GAMMA; k < HX_P_COUNT; k++)
+    for (int k = HX_P_CADYN_GAMMA; k < kLibKindEnd; k++)
         ctx->kmap_h[k].assign(std::max(ctx->lib_n[hx_lib_type_of_kind(k)], 1), 0);
     int nst = 0;
     for (int gi = 0; gi < nn; gi++) {
@@ -257,7 +261,7 @@ int hx_lib_load(hx_ctx* ctx, const hx_group_desc* desc) {
     HXC(ctx->lib_ent_st.upload(ent_st, st));
     HXC(ctx->lib_ent_fix.upload(ent_fix, st));
     HXC(ctx->lib_fix.upload(fix, st));
-    for (int k = HX_P_CADYN_GAMMA; k < HX_P_COUNT; k++) {
+    for (int k = HX_P_CADYN_GAMMA; k < kLibKindEnd; k++) {
         HXC(ctx->kmap[k].upload(ctx->kmap_h[k], st));
         HXC(ctx->prm[k].upload(prm[k - HX_P_CADYN_GAMMA], st));
     }

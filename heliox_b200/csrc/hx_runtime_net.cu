@@ -73,7 +73,9 @@ int hx_net_load(hx_ctx* ctx, const hx_group_desc* d) {
     ctx->nsyn = ctx->nexp + ctx->nexp2;
     ctx->nstim = std::max(d->nnetstim, 0);
     ctx->nhg = std::max(d->nhalfgap, 0);
-    ctx->ngj = std::max(d->ngapj, 0);
+    ctx->ngj_lr = std::max(d->ngapj, 0);
+    ctx->ngnp = std::max(d->ngapnp, 0);
+    ctx->ngj = ctx->ngj_lr + ctx->ngnp;
     ctx->ngr = std::max(d->ngraded, 0);
     ctx->gid_base = d->gid_base;
     ctx->nsrc_cells = d->nsrc_cells > 0 ? d->nsrc_cells : d->ncell;
@@ -97,8 +99,9 @@ int hx_net_load(hx_ctx* ctx, const hx_group_desc* d) {
         return false;
     };
     if (bad_node(d->expsyn_node, ctx->nexp) || bad_node(d->exp2syn_node, ctx->nexp2) ||
-        bad_node(d->hg_node, ctx->nhg) || bad_node(d->hg_src, ctx->nhg) || bad_node(d->gj_node, ctx->ngj) ||
-        bad_node(d->gj_pre, ctx->ngj) || bad_node(d->gr_node, ctx->ngr) || bad_node(d->gr_pre, ctx->ngr))
+        bad_node(d->hg_node, ctx->nhg) || bad_node(d->hg_src, ctx->nhg) || bad_node(d->gj_node, ctx->ngj_lr) ||
+        bad_node(d->gj_pre, ctx->ngj_lr) || bad_node(d->gn_node, ctx->ngnp) || bad_node(d->gn_src, ctx->ngnp) ||
+        bad_node(d->gr_node, ctx->ngr) || bad_node(d->gr_pre, ctx->ngr))
         return hx_fail(ctx, "network node index out of range");
     // ---- exponential synapses
     std::vector<Ord> so;
@@ -200,7 +203,14 @@ int hx_net_load(hx_ctx* ctx, const hx_group_desc* d) {
         std::sort(v.begin(), v.end());
         return v;
     };
-    std::vector<Ord> ho = order(ctx->nhg, d->hg_node), jo = order(ctx->ngj, d->gj_node), ro = order(ctx->ngr, d->gr_node);
+    std::vector<Ord> ho = order(ctx->nhg, d->hg_node), ro = order(ctx->ngr, d->gr_node);
+    // gapjunction_lr and gapjunction_noptr instances in one array: by node,
+    // then mechanism (the reference's current order on a node), then instance
+    std::vector<Ord> jo;
+    jo.reserve(ctx->ngj);
+    for (int i = 0; i < ctx->ngj_lr; i++) jo.push_back(Ord{P.ref2gpu[d->gj_node[i]], 0, i});
+    for (int i = 0; i < ctx->ngnp; i++) jo.push_back(Ord{P.ref2gpu[d->gn_node[i]], 1, i});
+    std::sort(jo.begin(), jo.end());
     auto gather_d = [](const std::vector<Ord>& v, const double* a) {
         std::vector<double> out(std::max<size_t>(v.size(), 1), 0.0);
         for (size_t i = 0; i < v.size(); i++) out[i] = a[v[i].ref];
@@ -219,20 +229,38 @@ int hx_net_load(hx_ctx* ctx, const hx_group_desc* d) {
     HXC(ctx->node_hg_off.upload(csr_by_node(ho, nn), st));
     HXC(ctx->node_gj_off.upload(csr_by_node(jo, nn), st));
     HXC(ctx->node_gr_off.upload(csr_by_node(ro, nn), st));
-    std::vector<int> hs = partner(ho, d->hg_src), jp = partner(jo, d->gj_pre), rp = partner(ro, d->gr_pre);
+    std::vector<int> hs = partner(ho, d->hg_src), rp = partner(ro, d->gr_pre);
+    std::vector<int> jp(std::max<size_t>(jo.size(), 1), 0);
+    std::vector<double> jg(std::max<size_t>(jo.size(), 1), 0.0), jw(std::max<size_t>(jo.size(), 1), 0.0);
+    std::vector<int> jmap_lr(std::max(ctx->ngj_lr, 1), 0), jmap_np(std::max(ctx->ngnp, 1), 0);
+    for (size_t q = 0; q < jo.size(); q++) {
+        const int r = jo[q].ref;
+        if (jo[q].kord == 0) {
+            jp[q] = P.ref2gpu[d->gj_pre[r]];
+            jg[q] = d->gj_g[r];
+            jw[q] = d->gj_w[r];
+            jmap_lr[r] = (int)q;
+        } else {  // i = weight (v - vpre) is w (g (v - vpre)) with g = weight, w = 1, bit for bit
+            jp[q] = P.ref2gpu[d->gn_src[r]];
+            jg[q] = d->gn_weight[r];
+            jw[q] = 1.0;
+            jmap_np[r] = (int)q;
+        }
+    }
     HXC(ctx->hg_src.upload(hs, st));
     HXC(ctx->gj_pre.upload(jp, st));
     HXC(ctx->gr_pre.upload(rp, st));
     HXC(ctx->prm[HX_P_HALFGAP_G].upload(gather_d(ho, d->hg_g), st));
-    HXC(ctx->prm[HX_P_GAPJ_G].upload(gather_d(jo, d->gj_g), st));
-    HXC(ctx->prm[HX_P_GAPJ_W].upload(gather_d(jo, d->gj_w), st));
+    HXC(ctx->prm[HX_P_GAPJ_G].upload(jg, st));
+    HXC(ctx->prm[HX_P_GAPJ_W].upload(jw, st));
     HXC(ctx->prm[HX_P_GRADED_W].upload(gather_d(ro, d->gr_w), st));
     HXC(ctx->gr_delta.upload(gather_d(ro, d->gr_delta), st));
     HXC(ctx->gr_vth.upload(gather_d(ro, d->gr_vth), st));
     for (auto* b : {&ctx->gr_g, &ctx->gr_k, &ctx->gr_erev, &ctx->gr_s, &ctx->lS}) HXC(b->ensure(std::max(ctx->ngr, 1)));
     ctx->kmap_h[HX_P_HALFGAP_G] = kmap_of(ho);
-    ctx->kmap_h[HX_P_GAPJ_G] = kmap_of(jo);
-    ctx->kmap_h[HX_P_GAPJ_W] = kmap_of(jo);
+    ctx->kmap_h[HX_P_GAPJ_G] = jmap_lr;
+    ctx->kmap_h[HX_P_GAPJ_W] = jmap_lr;
+    ctx->kmap_h[HX_P_GAPNP_W] = jmap_np;
     ctx->kmap_h[HX_P_GRADED_W] = kmap_of(ro);
     // incoming partner contributions per node: (kind << 28 | instance), kind-major
     {

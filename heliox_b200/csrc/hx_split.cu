@@ -32,8 +32,6 @@
 
 namespace hx {
 
-constexpr long long kSpinLimit = 20000000LL;  // x ~100 ns sleeps: ~2 s before a barrier gives up
-
 // Grid barrier over the cooperative launch.  gen: the generation this CTA
 // expects to see released (kept by thread 0).
 __device__ __forceinline__ void grid_sync(const DevSplit& X, unsigned& gen) {
@@ -51,7 +49,7 @@ __device__ __forceinline__ void grid_sync(const DevSplit& X, unsigned& gen) {
             } else {
                 long long it = 0;
                 while (*vgen == gen && *verr == 0) {
-                    if (++it > kSpinLimit) {
+                    if (++it > X.spin_limit) {
                         atomicOr(X.err, 1);
                         break;
                     }

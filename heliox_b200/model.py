@@ -17,7 +17,7 @@ Mechanism order inside one step is the order of the CoreNEURON mechanism list
 that the reference keeps in ``mech_current_list``
 (``src/io/coredat_to_innerdat.cpp:179-181``); the exporter here writes it as
 capacitance, pas, hh, IClamp, ExpSyn, Exp2Syn, NetStim, HalfGap,
-gapjunction_lr, neuron_to_neuron_syn_lr.
+gapjunction_lr, gapjunction_noptr, neuron_to_neuron_syn_lr.
 
 Network parts (all optional, empty by default):
 
@@ -36,6 +36,9 @@ Network parts (all optional, empty by default):
   whose voltage is copied into vgap; HalfGap.cu, simulate.cpp:953-966);
 * ``gapjunction``: gapjunction_lr (fields g, w, ``ifields['pre']``,
   gapjunction_lr.cu:58-65);
+* ``gapnoptr``: gapjunction_noptr (field weight, ``ifields['src']`` the node
+  whose voltage the reference's gap transfer copies into vpre after every
+  update; i = weight (v - vpre), worm-mech/gapjunction_noptr.cu:33-36);
 * ``graded``: neuron_to_neuron_syn_lr (fields w, g, delta, k, Vth, erev,
   dvpre, ``ifields['pre']``, neuron_to_neuron_syn_lr.cu:97-145).
 """
@@ -59,6 +62,7 @@ EXP2SYN_FIELDS = ("tau1", "tau2", "e", "delay", "weight")
 NETSTIM_FIELDS = ("interval", "number", "start", "noise")
 HALFGAP_FIELDS = ("g",)
 GAPJ_FIELDS = ("g", "w")
+GAPNP_FIELDS = ("weight",)
 GRADED_FIELDS = ("w", "g", "delta", "k", "Vth", "erev", "dvpre")
 SPIKE_THRESHOLD = 10.0
 
@@ -223,6 +227,7 @@ class CellGroup:
     netstim: Optional[MechTable] = None
     halfgap: Optional[MechTable] = None
     gapjunction: Optional[MechTable] = None
+    gapnoptr: Optional[MechTable] = None
     graded: Optional[MechTable] = None
     ps_thresh: Optional[np.ndarray] = None
     netstim_rng: int = 0
@@ -239,6 +244,8 @@ class CellGroup:
             self.halfgap = empty_table(HALFGAP_FIELDS, ("src",))
         if self.gapjunction is None:
             self.gapjunction = empty_table(GAPJ_FIELDS, ("pre",))
+        if self.gapnoptr is None:
+            self.gapnoptr = empty_table(GAPNP_FIELDS, ("src",))
         if self.graded is None:
             self.graded = empty_table(GRADED_FIELDS, ("pre",))
         if self.ps_thresh is None:
@@ -248,12 +255,12 @@ class CellGroup:
     def has_network(self) -> bool:
         """True if any event, gap or graded coupling is present."""
         return bool(self.expsyn.n or self.exp2syn.n or self.netstim.n or self.halfgap.n or self.gapjunction.n
-                    or self.graded.n)
+                    or self.gapnoptr.n or self.graded.n)
 
     @property
     def coupled(self) -> bool:
         """True if voltages of other nodes enter a step's currents or states (gaps, graded synapses)."""
-        return bool(self.halfgap.n or self.gapjunction.n or self.graded.n)
+        return bool(self.halfgap.n or self.gapjunction.n or self.gapnoptr.n or self.graded.n)
 
     # ------------------------------------------------------------------ basics
     @property
@@ -303,6 +310,7 @@ class CellGroup:
         for tab, nm, fl in ((self.expsyn, "ExpSyn", EXPSYN_FIELDS), (self.exp2syn, "Exp2Syn", EXP2SYN_FIELDS),
                             (self.halfgap, "HalfGap", HALFGAP_FIELDS), (self.gapjunction, "gapjunction_lr",
                                                                         GAPJ_FIELDS),
+                            (self.gapnoptr, "gapjunction_noptr", GAPNP_FIELDS),
                             (self.graded, "neuron_to_neuron_syn_lr", GRADED_FIELDS)):
             if tab.n and (np.any(tab.nodes < 0) or np.any(tab.nodes >= n)):
                 raise ValueError(f"{nm} node index out of range")
@@ -322,6 +330,7 @@ class CellGroup:
             if tab.n and np.any(tab.fields["delay"] < self.dt):
                 raise ValueError(f"{nm}: NetCon delays must be at least dt (one step)")
         for tab, nm, key in ((self.halfgap, "HalfGap", "src"), (self.gapjunction, "gapjunction_lr", "pre"),
+                             (self.gapnoptr, "gapjunction_noptr", "src"),
                              (self.graded, "neuron_to_neuron_syn_lr", "pre")):
             pv = tab.ifields.get(key)
             if pv is None or (tab.n and (np.any(pv < 0) or np.any(pv >= n))):
@@ -400,6 +409,7 @@ class CellGroup:
             netstim=self.netstim.copy(),
             halfgap=self.halfgap.copy(),
             gapjunction=self.gapjunction.copy(),
+            gapnoptr=self.gapnoptr.copy(),
             graded=self.graded.copy(),
             ps_thresh=self.ps_thresh.copy(),
             netstim_rng=self.netstim_rng,
@@ -411,7 +421,8 @@ class CellGroup:
         """The live array of one learnable/settable parameter."""
         tab = {"hh": self.hh, "pas": self.pas, "IClamp": self.iclamp, "ExpSyn": self.expsyn,
                "Exp2Syn": self.exp2syn, "NetStim": self.netstim, "HalfGap": self.halfgap,
-               "gapjunction_lr": self.gapjunction, "neuron_to_neuron_syn_lr": self.graded}.get(mech)
+               "gapjunction_lr": self.gapjunction, "gapjunction_noptr": self.gapnoptr,
+               "neuron_to_neuron_syn_lr": self.graded}.get(mech)
         if tab is None:
             if mech == "capacitance" and var == "cm":
                 return self.cm

@@ -35,6 +35,7 @@ _MECH_VAR = {
     ("HalfGap", "g"): "HalfGap.g",
     ("gapjunction_lr", "g"): "gapjunction_lr.g",
     ("gapjunction_lr", "w"): "gapjunction_lr.w",
+    ("gapjunction_noptr", "weight"): "gapjunction_noptr.weight",
     ("neuron_to_neuron_syn_lr", "w"): "neuron_to_neuron_syn_lr.w",
 }
 # library mechanisms: every HX_P key "<mech>.<var>" is also its handle name
@@ -148,7 +149,8 @@ class Sim:
         g = self.group
         mech = key.split(".")[0]
         tab = {"hh": g.hh, "pas": g.pas, "IClamp": g.iclamp, "ExpSyn": g.expsyn, "Exp2Syn": g.exp2syn,
-               "HalfGap": g.halfgap, "gapjunction_lr": g.gapjunction, "neuron_to_neuron_syn_lr": g.graded}.get(mech)
+               "HalfGap": g.halfgap, "gapjunction_lr": g.gapjunction, "gapjunction_noptr": g.gapnoptr,
+               "neuron_to_neuron_syn_lr": g.graded}.get(mech)
         if key == "cm":
             return g.nnode
         if tab is None:
@@ -192,6 +194,10 @@ class Sim:
         self._xfn = _lib.EXCHANGE_FN(cb)
         self._check(self._L.hx_set_exchange(self._ctx, self._xfn, None, int(nranks), int(cap_entries)),
                     "hx_set_exchange")
+
+    def set_split_barrier_limit(self, sleeps: int = 0):
+        """Bound of a split-cell grid-barrier wait, in ~100 ns sleeps (0 = default, ~2 s)."""
+        self._check(self._L.hx_set_split_barrier_limit(self._ctx, int(sleeps)), "hx_set_split_barrier_limit")
 
     def set_window(self, steps: int):
         self._check(self._L.hx_set_window(self._ctx, int(steps)), "hx_set_window")

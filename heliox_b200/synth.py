@@ -577,7 +577,8 @@ def network_config4_shard(total: int, rank: int, nranks: int, seed: int = 4, syn
 
 def coupled_network(ncell: int = 6, seed: int = 5, nmin: int = 50, nmax: int = 150, ngap: int = 6,
                     ngapj: int = 3, ngraded: int = 10, drive_frac: float = 0.4,
-                    gap_g: Tuple[float, float] = (1e-4, 1e-3), graded_w: Tuple[float, float] = (2e-4, 2e-3)) -> CellGroup:
+                    gap_g: Tuple[float, float] = (1e-4, 1e-3), graded_w: Tuple[float, float] = (2e-4, 2e-3),
+                    ngapnp: int = 0) -> CellGroup:
     """Config 5 style network: cells coupled by gap junctions and graded synapses.
 
     ``ngap`` HalfGap pairs (two instances per pair at random nodes of two
@@ -585,8 +586,10 @@ def coupled_network(ncell: int = 6, seed: int = 5, nmin: int = 50, nmax: int = 1
     ``ngapj`` gapjunction_lr pairs (w 1, g U[gap_g]), ``ngraded``
     neuron_to_neuron_syn_lr synapses from a random cell's soma onto a random
     node of another cell (w = +-U[graded_w], 80 % positive; delta 5 mV,
-    Vth -20 mV, the MOD defaults otherwise).  A fraction ``drive_frac`` of the
-    cells keep their somatic IClamp.
+    Vth -20 mV, the MOD defaults otherwise), ``ngapnp`` gapjunction_noptr
+    pairs (weight U[gap_g], vpre from the partner node; drawn after the others,
+    so the rest of the network does not depend on it).  A fraction
+    ``drive_frac`` of the cells keep their somatic IClamp.
     """
     rng = np.random.default_rng(seed)
     cells = [random_tree_cell(seed * 1000 + c, nmin=nmin, nmax=nmax) for c in range(ncell)]
@@ -624,6 +627,15 @@ def coupled_network(ncell: int = 6, seed: int = 5, nmin: int = 50, nmax: int = 1
         rp.append(a)
         w = float(rng.uniform(*graded_w))
         rw.append(w if rng.random() < 0.8 else -w)
+    nn_, ns_, nw_ = [], [], []
+    for _ in range(ngapnp):
+        a, b = two_cells()
+        na, nb = int(rng.choice(per_cell[a])), int(rng.choice(per_cell[b]))
+        gg = float(rng.uniform(*gap_g))
+        nn_ += [na, nb]
+        ns_ += [nb, na]
+        nw_ += [gg, gg]
+    g.gapnoptr = _table(nn_, {"weight": nw_}, {"src": ns_})
     g.halfgap = _table(hn, {"g": hg}, {"src": hs})
     g.gapjunction = _table(jn, {"g": jg, "w": np.ones(len(jn))}, {"pre": jp})
     ng = len(rn)

@@ -20,7 +20,7 @@
 extern "C" {
 #endif
 
-#define HX_ABI_VERSION 7
+#define HX_ABI_VERSION 8
 
 typedef struct hx_ctx hx_ctx;
 
@@ -194,6 +194,12 @@ typedef struct hx_group_desc {
     int ngapj;
     const int *gj_node, *gj_pre;
     const double *gj_g, *gj_w;
+    /* gapjunction_noptr (src/mech/worm-mech/gapjunction_noptr.cu:33-36):
+     * i = weight (v - vpre), vpre copied from v of node gn_src by the
+     * reference's gap transfer (simulate.cpp:953-966) */
+    int ngapnp;
+    const int *gn_node, *gn_src;
+    const double* gn_weight;
     /* neuron_to_neuron_syn_lr (src/mech/worm-lr-mech/neuron_to_neuron_syn_lr.cu) */
     int ngraded;
     const int *gr_node, *gr_pre;
@@ -265,7 +271,8 @@ enum hx_param_kind {
     HX_P_CCA1_G = 55,
     HX_P_EGL19_G = 56,
     HX_P_UNC2_G = 57,
-    HX_P_COUNT = 58
+    HX_P_GAPNP_W = 58, /* gapjunction_noptr weight per instance */
+    HX_P_COUNT = 59
 };
 
 /* Statistics of the execution plan built at load time. */
@@ -302,6 +309,15 @@ int hx_set_pack_target(hx_ctx* ctx, int nodes_per_warp);
  * does not fit, the backward recomputes checkpointed segments.  0 = default
  * (60% of free device memory at load time). */
 int hx_set_tape_budget(hx_ctx* ctx, size_t bytes);
+/* How long a grid-barrier wait of the split-cell kernels (a cell larger than
+ * one CTA) lasts before it gives up: `sleeps` waits of ~100 ns (0 = default,
+ * 20,000,000: ~2 s).  A wait that gives up sets an error flag, later barriers
+ * return at once, the launch finishes, and the forward or backward returns -1
+ * with "a grid barrier of the split-cell kernels timed out"; the context stays
+ * usable.  Takes effect at the next launch.  (The reference's intra-cell
+ * parallel solvers synchronise inside one kernel, simulate.cu:119-189; this
+ * bounds the cross-CTA form.) */
+int hx_set_split_barrier_limit(hx_ctx* ctx, long long sleeps);
 
 /* ---- model ---------------------------------------------------------------- */
 /* Replaces SimRuntimeCore::load_model -> read_coredat -> data_format_trans

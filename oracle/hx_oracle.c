@@ -22,6 +22,7 @@
  *   HalfGap + gap transfer            src/mech/user-mech/HalfGap.cu:56-68,
  *                                     simulate.cpp:953-966
  *   gapjunction_lr                    src/mech/worm-lr-mech/gapjunction_lr.cu:58-65
+ *   gapjunction_noptr (gap transfer)  src/mech/worm-mech/gapjunction_noptr.cu:33-36
  *   neuron_to_neuron_syn_lr           src/mech/worm-lr-mech/neuron_to_neuron_syn_lr.cu:97-145
  * and the discrete adjoint of that step sequence (no reference counterpart).
  * The adjoint holds the spike/event schedule of the forward fixed (events are
@@ -242,6 +243,7 @@ typedef struct {
     double *ns_event, *ns_on, *ns_ispike, *ns_noise;
     ran123 rng;
     double* vgap;      /* HalfGap vgap */
+    double* vpre_np;   /* gapjunction_noptr vpre */
     double *gr_s, *gr_g, *gr_k, *gr_erev;
     /* event recording for the adjoint: (step, synapse) of every delivery */
     int rec_step; /* step whose deliveries are being recorded, -1 = off */
@@ -290,13 +292,15 @@ static int state_alloc(const hxo_group* g, hxo_state* s) {
         s->ns_ispike = (double*)calloc(nst, sizeof(double));
         s->ns_noise = (double*)calloc(nst, sizeof(double));
         s->vgap = (double*)calloc((size_t)N->nhg + 1, sizeof(double));
+        s->vpre_np = (double*)calloc((size_t)N->ngn + 1, sizeof(double));
         size_t ng = (size_t)N->ngr + 1;
         s->gr_s = (double*)calloc(ng, sizeof(double));
         s->gr_g = (double*)calloc(ng, sizeof(double));
         s->gr_k = (double*)calloc(ng, sizeof(double));
         s->gr_erev = (double*)calloc(ng, sizeof(double));
         if (!(s->sA && s->sB && s->s_tau1 && s->s_factor && s->spk_flag && s->spk_t && s->pre_flag && s->ns_event &&
-              s->ns_on && s->ns_ispike && s->ns_noise && s->vgap && s->gr_s && s->gr_g && s->gr_k && s->gr_erev))
+              s->ns_on && s->ns_ispike && s->ns_noise && s->vgap && s->vpre_np && s->gr_s && s->gr_g && s->gr_k &&
+              s->gr_erev))
             return -1;
     }
     return 0;
@@ -323,6 +327,7 @@ static void state_free(hxo_state* s) {
     free(s->ns_ispike);
     free(s->ns_noise);
     free(s->vgap);
+    free(s->vpre_np);
     free(s->gr_s);
     free(s->gr_g);
     free(s->gr_k);
@@ -524,14 +529,20 @@ static double gr_inf(const hxo_net* N, int j, double v) {
     return 1.0 / (1.0 + exp((N->gr_vth[j] - v) / N->gr_delta[j]));
 }
 
+/* gap_transfer_cpu, simulate.cpp:953-966: every wired target (HalfGap vgap,
+ * gapjunction_noptr vpre) takes the voltage of its source node */
+static void gap_transfer(const hxo_net* N, hxo_state* s, const double* v) {
+    for (int j = 0; j < N->nhg; j++) s->vgap[j] = v[N->hg_src[j]];
+    for (int j = 0; j < N->ngn; j++) s->vpre_np[j] = v[N->gn_src[j]];
+}
+
 /* finitialize_cpu, simulate.cpp:271-339: v = v_init, gap transfer, mech INITIAL
  * in mech_current_list order, then one spike delivery at t = 0. */
 static void finitialize(const hxo_group* g, hxo_state* s, double v_init) {
     s->t = 0;
     for (int i = 0; i < g->nnode; i++) s->v[i] = v_init;
     const hxo_net* N = g->net;
-    if (N)
-        for (int j = 0; j < N->nhg; j++) s->vgap[j] = s->v[N->hg_src[j]];
+    if (N) gap_transfer(N, s, s->v);
     for (int j = 0; j < g->nhh; j++) {
         hh_rates_t r;
         hh_rates(s->v[g->hh_node[j]], g->celsius, &r);
@@ -595,7 +606,8 @@ static void pp_add(double* rhs, double* d, int i, double i1, double i0, double a
 
 /* setup_tree_matrix_cpu, simulate.cpp:455-556, mechanisms in the exported
  * mechanism-list order (capacitance, pas, hh, IClamp, ExpSyn, Exp2Syn,
- * NetStim (no current), HalfGap, gapjunction_lr, neuron_to_neuron_syn_lr). */
+ * NetStim (no current), HalfGap, gapjunction_lr, gapjunction_noptr,
+ * neuron_to_neuron_syn_lr). */
 static void setup_tree_matrix(const hxo_group* g, hxo_state* s) {
     const int nn = g->nnode;
     double* v = s->v;
@@ -658,6 +670,12 @@ static void setup_tree_matrix(const hxo_group* g, hxo_state* s) {
             int i = N->gj_node[j];
             double vp = v[N->gj_pre[j]], gg = N->gj_g[j], w = N->gj_w[j];
             pp_add(rhs, d, i, w * (gg * ((v[i] + FD_EPS) - vp)), w * (gg * (v[i] - vp)), g->area[i], 0);
+        }
+        /* gapjunction_noptr: i = weight (v - vpre) (worm-mech/gapjunction_noptr.cu:33-36) */
+        for (int j = 0; j < N->ngn; j++) {
+            int i = N->gn_node[j];
+            double vp = s->vpre_np[j], ww = N->gn_w[j];
+            pp_add(rhs, d, i, ww * ((v[i] + FD_EPS) - vp), ww * (v[i] - vp), g->area[i], 0);
         }
         /* neuron_to_neuron_syn_lr: i = |w| (g s (v - erev)) */
         for (int j = 0; j < N->ngr; j++) {
@@ -758,8 +776,7 @@ static void fadvance(const hxo_group* g, hxo_state* s) {
     setup_tree_matrix(g, s);
     solve_serial(g, s->d, s->rhs);
     for (int i = 0; i < g->nnode; i++) s->v[i] += s->rhs[i];
-    if (g->net)
-        for (int j = 0; j < g->net->nhg; j++) s->vgap[j] = s->v[g->net->hg_src[j]];
+    if (g->net) gap_transfer(g->net, s, s->v);
     s->t += 0.5 * g->dt;
     nonvint(g, s);
 }
@@ -885,8 +902,7 @@ int hxo_adjoint(const hxo_group* g, double v_init, int nstep, int nprobe, const 
         setup_tree_matrix(g, &s);
         solve_serial(g, s.d, s.rhs);
         for (int i = 0; i < nn; i++) s.v[i] += s.rhs[i];
-        if (N)
-            for (int j = 0; j < N->nhg; j++) s.vgap[j] = s.v[N->hg_src[j]];
+        if (N) gap_transfer(N, &s, s.v);
         s.t += 0.5 * g->dt;
         nonvint(g, &s);
         if (trace) record(g, &s, nprobe, probe, trace + (size_t)(k + 1) * nprobe);
@@ -917,6 +933,7 @@ int hxo_adjoint(const hxo_group* g, double v_init, int nstep, int nprobe, const 
             zero_if(gr->gj_g, N->ngj);
             zero_if(gr->gj_w, N->ngj);
             zero_if(gr->gr_w, N->ngr);
+            zero_if(gr->gn_w, N->ngn);
         }
     }
     const double dt = g->dt;
@@ -985,8 +1002,7 @@ int hxo_adjoint(const hxo_group* g, double v_init, int nstep, int nprobe, const 
             memcpy(s.sB, tB + (size_t)k * nsyn, sizeof(double) * nsyn);
         }
         if (ngr) memcpy(s.gr_s, tS + (size_t)k * ngr, sizeof(double) * ngr);
-        if (N)
-            for (int j = 0; j < N->nhg; j++) s.vgap[j] = vk[N->hg_src[j]];
+        if (N) gap_transfer(N, &s, vk);
         setup_tree_matrix(g, &s);
         memcpy(dd, s.d, sizeof(double) * nn);
         /* w = M_k^{-T} mu */
@@ -1060,6 +1076,14 @@ int hxo_adjoint(const hxo_group* g, double v_init, int nstep, int nprobe, const 
                 GADD(gj_g, j, -w[i] * sa * ww * dv + ld * sa * ww);
                 lv[i] += -w[i] * sa * ww * gg;
                 lv[q] += w[i] * sa * ww * gg;
+            }
+            for (int j = 0; j < N->ngn; j++) {
+                int i = N->gn_node[j], q = N->gn_src[j];
+                double sa = 1.e2 / g->area[i], ww = N->gn_w[j];
+                double ld = -w[i] * (vk1[i] - vk[i]);
+                GADD(gn_w, j, -w[i] * sa * (vk[i] - vk[q]) + ld * sa);
+                lv[i] += -w[i] * sa * ww;
+                lv[q] += w[i] * sa * ww;
             }
             for (int j = 0; j < ngr; j++) {
                 int i = N->gr_node[j];

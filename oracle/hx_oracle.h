@@ -41,6 +41,9 @@ typedef struct hxo_net {
     int ngj;
     const int *gj_node, *gj_pre;
     const double *gj_g, *gj_w;
+    int ngn; /* gapjunction_noptr: vpre copied from v of node gn_src by the gap transfer */
+    const int *gn_node, *gn_src;
+    const double* gn_w;
     int ngr;
     const int *gr_node, *gr_pre;
     const double *gr_w, *gr_g, *gr_delta, *gr_k, *gr_vth, *gr_erev;
@@ -119,6 +122,7 @@ typedef struct hxo_grads {
     double *ic_amp;
     double *exp_w, *exp_e, *exp2_w, *exp2_e; /* per ExpSyn / Exp2Syn instance */
     double *hg_g, *gj_g, *gj_w, *gr_w;       /* per HalfGap / gapjunction_lr / graded instance */
+    double* gn_w;                            /* per gapjunction_noptr instance */
 } hxo_grads;
 
 /* Forward: finitialize(v_init) then nstep fadvance steps.

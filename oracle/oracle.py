@@ -31,6 +31,7 @@ class _Net(C.Structure):
         ("rng_mode", C.c_int),
         ("nhg", C.c_int), ("hg_node", _ip), ("hg_src", _ip), ("hg_g", _dp),
         ("ngj", C.c_int), ("gj_node", _ip), ("gj_pre", _ip), ("gj_g", _dp), ("gj_w", _dp),
+        ("ngn", C.c_int), ("gn_node", _ip), ("gn_src", _ip), ("gn_w", _dp),
         ("ngr", C.c_int), ("gr_node", _ip), ("gr_pre", _ip), ("gr_w", _dp), ("gr_g", _dp), ("gr_delta", _dp),
         ("gr_k", _dp), ("gr_vth", _dp), ("gr_erev", _dp),
         ("spike_cap", C.c_int), ("spike_gid", _ip), ("spike_t", _dp), ("nspike", C.c_int),
@@ -91,6 +92,7 @@ class _Grads(C.Structure):
         ("ic_amp", _dp),
         ("exp_w", _dp), ("exp_e", _dp), ("exp2_w", _dp), ("exp2_e", _dp),
         ("hg_g", _dp), ("gj_g", _dp), ("gj_w", _dp), ("gr_w", _dp),
+        ("gn_w", _dp),
     ]
 
 
@@ -329,6 +331,8 @@ class _Bound:
             gj = g.gapjunction
             n.ngj, n.gj_node, n.gj_pre = gj.n, I(gj.nodes), I(gj.ifields["pre"])
             n.gj_g, n.gj_w = D(gj.fields["g"]), D(gj.fields["w"])
+            gn = g.gapnoptr
+            n.ngn, n.gn_node, n.gn_src, n.gn_w = gn.n, I(gn.nodes), I(gn.ifields["src"]), D(gn.fields["weight"])
             gr = g.graded
             n.ngr, n.gr_node, n.gr_pre = gr.n, I(gr.nodes), I(gr.ifields["pre"])
             n.gr_w, n.gr_g, n.gr_delta, n.gr_k, n.gr_vth, n.gr_erev = (
@@ -414,7 +418,7 @@ def forward_lib(g, nstep: int, probe: Optional[Sequence[int]] = None, v_init: Op
 
 GRAD_KEYS = ("hh.gnabar", "hh.gkbar", "hh.gl", "hh.el", "pas.g", "pas.e", "cm", "IClamp.amp")
 NET_GRAD_KEYS = ("ExpSyn.weight", "ExpSyn.e", "Exp2Syn.weight", "Exp2Syn.e", "HalfGap.g", "gapjunction_lr.g",
-                 "gapjunction_lr.w", "neuron_to_neuron_syn_lr.w")
+                 "gapjunction_lr.w", "neuron_to_neuron_syn_lr.w", "gapjunction_noptr.weight")
 
 
 def adjoint(g, nstep: int, dLdv: np.ndarray, probe: Optional[Sequence[int]] = None, v_init: Optional[float] = None):
@@ -442,10 +446,10 @@ def adjoint(g, nstep: int, dLdv: np.ndarray, probe: Optional[Sequence[int]] = No
     gs.pas_g, gs.pas_e, gs.cm, gs.ic_amp = (_d(out[k]) for k in GRAD_KEYS[4:])
     if g.has_network:
         sizes = (g.expsyn.n, g.expsyn.n, g.exp2syn.n, g.exp2syn.n, g.halfgap.n, g.gapjunction.n, g.gapjunction.n,
-                 g.graded.n)
+                 g.graded.n, g.gapnoptr.n)
         for k, nsz in zip(NET_GRAD_KEYS, sizes):
             out[k] = np.zeros(nsz)
-        gs.exp_w, gs.exp_e, gs.exp2_w, gs.exp2_e, gs.hg_g, gs.gj_g, gs.gj_w, gs.gr_w = (
+        gs.exp_w, gs.exp_e, gs.exp2_w, gs.exp2_e, gs.hg_g, gs.gj_g, gs.gj_w, gs.gr_w, gs.gn_w = (
             _d(out[k]) for k in NET_GRAD_KEYS)
     rc = L.hxo_adjoint(C.byref(b.s), float(g.v_init if v_init is None else v_init), int(nstep), int(probe.shape[0]),
                        _i(probe), _d(dLdv), _d(trace), C.byref(gs))

@@ -39,7 +39,7 @@ SRCS=$(cd "$REF" && ls \
   mech/worm-lr-mech/kcnl_lr.cu mech/worm-lr-mech/nca_lr.cu mech/worm-lr-mech/kqt3_lr.cu \
   mech/worm-lr-mech/cainternm_lr.cu mech/worm-mech/shl1.cu mech/worm-mech/kvs1.cu mech/worm-mech/irk.cu \
   mech/worm-mech/egl36.cu mech/worm-mech/shk1.cu mech/worm-mech/egl2.cu mech/worm-mech/cca1.cu \
-  mech/worm-mech/egl19.cu mech/worm-mech/unc2.cu \
+  mech/worm-mech/egl19.cu mech/worm-mech/unc2.cu mech/worm-mech/gapjunction_noptr.cu \
   2>/dev/null)
 
 compile() {

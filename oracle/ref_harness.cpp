@@ -39,6 +39,7 @@
 #include <cstdlib>
 #include <memory>
 #include <string>
+#include <tuple>
 #include <vector>
 
 #include "coredat_to_innerdat.h"
@@ -131,20 +132,22 @@ int main(int argc, char** argv) {
     data_format_trans(sim->neuron_group_list, arr, ngroup, mode, sim->dt);
     for (int i = 0; i < ngroup; i++) delete arr[i];
     sim->permute_type = ptype;
-    // HalfGap: vgap of instance i follows the voltage of a source node, wired
-    // through the reference's gap API (pairs written by the exporter)
-    {
-        FILE* f = std::fopen((dir + "/halfgap.i32").c_str(), "rb");
+    // HalfGap vgap and gapjunction_noptr vpre of instance i follow the voltage
+    // of a source node, wired through the reference's gap API (pairs written
+    // by the exporter)
+    for (const auto& [fname, mech, var] : {std::tuple<const char*, const char*, const char*>{"halfgap.i32", "HalfGap", "vgap"},
+                                           {"gapnoptr.i32", "gapjunction_noptr", "vpre"}}) {
+        FILE* f = std::fopen((dir + "/" + fname).c_str(), "rb");
         if (f && ptype != 0) {
-            std::fprintf(stderr, "HalfGap wiring needs permute type 0\n");
+            std::fprintf(stderr, "%s wiring needs permute type 0\n", mech);
             return 2;
         }
         if (f) {
             int pr[2];
             while (std::fread(pr, sizeof(int), 2, f) == 2) {
                 const int sid = sim->add_gap_source("global", "v", pr[1]);
-                if (sid < 0 || sim->add_gap_target(sid, "HalfGap", "vgap", pr[0]) != 0) {
-                    std::fprintf(stderr, "gap wiring failed for instance %d\n", pr[0]);
+                if (sid < 0 || sim->add_gap_target(sid, mech, var, pr[0]) != 0) {
+                    std::fprintf(stderr, "%s wiring failed for instance %d\n", mech, pr[0]);
                     return 4;
                 }
             }

@@ -33,6 +33,9 @@ CASES = {
                     2400, None),
     # HalfGap + gapjunction_lr + neuron_to_neuron_syn_lr coupling
     "net_coupled": (lambda: synth.coupled_network(), 2000, None),
+    # gapjunction_noptr (vpre through the gap transfer) on nodes that also carry
+    # HalfGap, gapjunction_lr and graded synapses: the per-node current order
+    "net_gapnoptr": (lambda: net_gapnoptr(), 2000, None),
     # user-mech channel set with calcium dynamics (spiking library cells)
     "lib_cells": (lambda: synth.lib_tree_batch(2, seed0=700, nmax=200), 2000, None),
     # hh cells and library cells in one group
@@ -40,6 +43,24 @@ CASES = {
     # library cells with the worm-lr calcium dynamics cainternm_lr
     "lib_cainternm": (lambda: synth.lib_tree_batch(2, seed0=710, nmax=200, cadyn="cainternm_lr"), 2000, None),
 }
+
+
+def net_gapnoptr():
+    """A coupled network plus gapjunction_noptr instances on every node that
+    carries a graded synapse, a gapjunction_lr or a HalfGap (weight
+    U[1e-4, 1e-3] uS, vpre from the root of the next cell), and five pairs at
+    random nodes."""
+    from heliox_b200.synth import _table
+
+    g = synth.coupled_network(ncell=5, seed=31, ngap=5, ngapj=4, ngraded=12, ngapnp=5)
+    cell = g.cell_of_node()
+    nodes = list(g.gapnoptr.nodes) + list(g.graded.nodes) + list(g.gapjunction.nodes) + list(g.halfgap.nodes)
+    src = list(g.gapnoptr.ifields["src"]) + [int(np.nonzero(cell == (cell[n] + 1) % g.ncell)[0][0])
+                                             for n in nodes[g.gapnoptr.n:]]
+    w = list(g.gapnoptr.fields["weight"]) + list(np.random.default_rng(1).uniform(1e-4, 1e-3, len(nodes) - g.gapnoptr.n))
+    g.gapnoptr = _table(nodes, {"weight": w}, {"src": src})
+    g.validate()
+    return g
 
 
 def _lib_mixed():

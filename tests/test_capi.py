@@ -38,7 +38,7 @@ def test_bindings_cover_header():
 
 
 def test_abi_version():
-    assert _lib.load().hx_abi_version() == 7
+    assert _lib.load().hx_abi_version() == 8
 
 
 def test_create_without_gpu_fails_loudly():

@@ -13,7 +13,7 @@ import pytest
 
 from heliox_b200 import coredat, synth
 
-TABLES = ("hh", "pas", "iclamp", "expsyn", "exp2syn", "netstim", "halfgap", "gapjunction", "graded")
+TABLES = ("hh", "pas", "iclamp", "expsyn", "exp2syn", "netstim", "halfgap", "gapjunction", "gapnoptr", "graded")
 
 
 def _same(g, h):
@@ -45,6 +45,7 @@ def _same(g, h):
         lambda: synth.random_tree_batch(6, seed0=17),
         lambda: synth.spiking_network(),
         lambda: synth.coupled_network(),
+        lambda: synth.coupled_network(ncell=4, seed=9, ngapnp=4),
         lambda: synth.lib_tree_batch(2, seed0=8, nmax=150),
         lambda: synth.lib_tree_batch(2, seed0=9, nmax=150, cadyn="cainternm_lr"),
         lambda: _lib_mixed(),

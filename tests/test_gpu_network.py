@@ -132,3 +132,34 @@ def test_network_parameters_roundtrip(Sim):
     tr = s.simulate(1200)
     ref, _ = O.forward(g2, 1200)
     _check_v(tr, ref)
+
+
+def test_gapjunction_noptr_forward_and_gradients(Sim):
+    """gapjunction_noptr (i = weight (v - vpre), vpre from the gap transfer) on
+    nodes that also carry HalfGap, gapjunction_lr and graded synapses (the
+    golden case net_gapnoptr, whose oracle trace is the reference's bit for
+    bit): voltages, spikes and every coupling gradient against the oracle, the
+    weights settable through the handle API."""
+    import importlib.util
+    import os
+
+    spec = importlib.util.spec_from_file_location(
+        "make_golden", os.path.join(os.path.dirname(__file__), "golden", "make_golden.py"))
+    mg = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mg)
+    g = mg.net_gapnoptr()
+    p = np.arange(g.nnode, dtype=np.int32)[::11]
+    s, tr, gg, ref, gr = _run(Sim, g, 1500, probes=p)
+    _check_v(tr, ref)
+    _check_spikes(s, gr["spikes"], g.dt)
+    _check_g(gg, gr, GRAD_KINDS + NET_KINDS + ("gapjunction_noptr.weight",))
+    assert np.max(np.abs(gr["gapjunction_noptr.weight"])) > 0
+    w = s.get_param_array("gapjunction_noptr.weight")
+    assert np.array_equal(w, g.gapnoptr.fields["weight"])
+    g2 = g.copy()
+    g2.gapnoptr.fields["weight"] = w * 1.7
+    s.set_param_array("gapjunction_noptr.weight", g2.gapnoptr.fields["weight"])
+    tr2 = s.simulate(600, probes=p)
+    ref2, _ = O.forward(g2, 600, probe=p)
+    _check_v(tr2, ref2)
+    s.close()

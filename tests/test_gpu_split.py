@@ -63,3 +63,27 @@ def test_giant_cell_forward(Sim):
     tr = s.simulate(300, probes=p)
     ref, _ = O.forward(g, 300, probe=p)
     assert np.max(np.abs(tr - ref)) / np.max(np.abs(ref)) <= V_TOL
+
+
+def test_split_barrier_wait_gives_up_and_context_recovers(Sim):
+    """A grid-barrier wait of the split kernels bounded to one ~100 ns sleep
+    runs out (148 CTAs never arrive within it at every barrier of 200 steps):
+    the wait sets the error flag, the remaining barriers return at once, the
+    launch finishes and the forward reports the timeout.  With the default
+    bound restored the same context runs the same forward to the oracle's
+    trace."""
+    from heliox_b200.runtime import HxError
+
+    g = synth.random_tree_cell(7, ncomp=6000, max_levels=40, amp=0.8)
+    p = _probes(g)
+    s = Sim(0)
+    s.load_group(g)
+    assert s.plan_stats()["nsub"] > 0
+    s.set_split_barrier_limit(1)
+    with pytest.raises(HxError, match="timed out"):
+        s.simulate(200, probes=p)
+    s.set_split_barrier_limit(0)
+    tr = s.simulate(200, probes=p)
+    ref, _ = O.forward(g, 200, probe=p)
+    assert np.max(np.abs(tr - ref)) / np.max(np.abs(ref)) <= V_TOL
+    s.close()

@@ -150,9 +150,9 @@ def test_network_adjoint_vs_fd_of_reference_forward():
     cases = (
         (synth.spiking_network(ncell=4, seed=3, nstim=2, weight=(0.02, 0.06)),
          (("exp2syn", "weight", "Exp2Syn.weight"), ("expsyn", "weight", "ExpSyn.weight"))),
-        (synth.coupled_network(ncell=4, seed=8, ngap=3, ngapj=2, ngraded=5),
+        (synth.coupled_network(ncell=4, seed=8, ngap=3, ngapj=2, ngraded=5, ngapnp=2),
          (("halfgap", "g", "HalfGap.g"), ("gapjunction", "w", "gapjunction_lr.w"),
-          ("graded", "w", "neuron_to_neuron_syn_lr.w"))),
+          ("graded", "w", "neuron_to_neuron_syn_lr.w"), ("gapnoptr", "weight", "gapjunction_noptr.weight"))),
     )
     for g, checks in cases:
         p = g.soma_nodes()
