@@ -146,6 +146,11 @@ struct hx_ctx {
     DevBuf<double> gr_g, gr_k, gr_erev, gr_delta, gr_vth, gr_s, tS, lS;
     DevBuf<double> vbuf;  // 2 x nnode ping-pong voltages of coupled launches
     DevBuf<double> xbuf;  // 2 x (nhg + ngj + ngr) partner contributions of coupled reverse launches
+    // grid-synchronous coupled launches: allowed (hx_set_grid_sync), and every
+    // pack co-resident with cooperative launch support (checked at load)
+    bool gsync_allowed = true, gsync_fit = false;
+    DevBuf<unsigned> gs_bar;
+    DevBuf<int> gs_err;
     DevBuf<double> tstart;
     DevBuf<int> ev_cnt, ev_syn, dev_err;
     int ev_cap = 0;

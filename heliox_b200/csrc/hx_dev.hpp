@@ -136,6 +136,18 @@ struct DevNet {
     double *x_hg_out, *x_gj_out, *x_gr_out;
     const double *x_hg_in, *x_gj_in, *x_gr_in;
     const int *node_in_off, *node_in;  // incoming (kind << 28 | instance) per node
+    // grid-synchronous coupled launches (cooperative, every pack co-resident):
+    // one launch runs many steps with one bounded grid barrier per step;
+    // v_k of every node in vbuf[k & 1] (forward), the reverse contributions
+    // of step k in xbuf[k & 1] (HalfGap, gapjunction, graded instances,
+    // xstride apart)
+    int gsync, nhg, ngj;
+    double* vbuf;
+    double* xbuf;
+    size_t xstride;
+    unsigned* gbar;    // arrival count, generation (zeroed before each launch)
+    int* gerr;         // set when a barrier wait gave up
+    long long gspin;   // sleeps of ~100 ns a wait takes before it gives up
 };
 
 // Library mechanisms of a group (step kernels instantiated with kLib = true).

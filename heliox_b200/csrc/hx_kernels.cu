@@ -64,8 +64,10 @@ __global__ void lib_init_kernel(DevLib L, int nnode, double v_init) {
 // delivery condition deliver_time <= t + dt/2 is resolved into the bucket
 // index when an event is routed), the network currents and the synapse /
 // graded-synapse state updates.  In a coupled launch (gaps, graded
-// synapses; one step) partner voltages come from N.vpeer and v_{k+1} goes to
-// N.vout, so that no CTA reads a value another CTA rewrites.
+// synapses) partner voltages come from N.vpeer and v_{k+1} goes to N.vout,
+// so that no CTA reads a value another CTA rewrites; a grid-synchronous
+// coupled launch (N.gsync, cooperative) runs many steps, v_k in
+// N.vbuf[k & 1], with one grid barrier after each step's v_{k+1} is stored.
 //
 // kLib adds the library mechanisms (hx_lib.cuh): their currents after the
 // other mechanisms in phase A, their state updates in phase C, and their
@@ -121,10 +123,20 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_kernel(DevGroup G, DevState S
     // kNet: the event count of the next step's bucket, read one step ahead
     // (all buckets of the launch's steps are routed before the launch)
     int ev_next = (kNet && k0 < k1) ? N.ev_cnt[(size_t)k0 * N.npack + p] : 0;
+    // grid-synchronous coupled launch: the CTA's active threads and barrier generation
+    const bool gs = kCpl && N.gsync;
+    int nact = 0;
+    unsigned gen = 0;
+    if (gs) {
+        const int s1 = G.pack_slot_off[p + 1] - 1;
+        nact = 32 * (G.cs_warp0[s1] + G.cs_nwarp[s1]);
+        if (threadIdx.x == 0) gen = *(volatile unsigned*)(N.gbar + 1);
+    }
     g.sync();
     if (k0 == 0 && trace)
         for (int q = q0 + g.tl; q < q1; q += g.nt) trace[P.slot[q]] = sv[P.local[q]];
     for (int k = k0; k < k1; ++k) {
+        const double* vpeer = kCpl ? (gs ? N.vbuf + (size_t)(k & 1) * (size_t)G.nnode : N.vpeer) : nullptr;
         // tape rows are written with streaming stores (evict first) so that the
         // row stream does not push the per-node parameters out of L2
         const size_t toff = (size_t)(k - T.k_base) * (size_t)G.nnode + pb;
@@ -206,7 +218,7 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_kernel(DevGroup G, DevState S
                         double sj = N.gr_s[j];
                         if (write_tape && k == T.k_base) N.tS[(size_t)j] = sj;  // row 0: s_{k_base - 1}
                         if (k > 0) {
-                            const double vpre = N.vpeer[__ldg(N.gr_pre + j)];
+                            const double vpre = __ldcg(vpeer + __ldg(N.gr_pre + j));
                             const double inf = 1.0 / (1.0 + exp((__ldg(N.gr_vth + j) - vpre) / __ldg(N.gr_delta + j)));
                             const double tau = (1.0 - inf) / __ldg(N.gr_k + j);
                             sj = inf + (sj - inf) * exp(-G.dt / tau);
@@ -216,7 +228,7 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_kernel(DevGroup G, DevState S
                     }
                 }
                 assemble<true, true, false, false, kCpl>(G, M, pb, i, fl, q, vi, sv, sa, sb, gm, gh, gn, tm, r, dd, N,
-                                                         N.sA, N.sB, sp, N.gr_s, N.vpeer);
+                                                         N.sA, N.sB, sp, N.gr_s, vpeer);
             } else if (kLib) {
                 double ica;
                 assemble<true, false, false, true>(G, M, pb, i, fl, q, vi, sv, sa, sb, gm, gh, gn, tm, r, dd, N,
@@ -255,6 +267,11 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_kernel(DevGroup G, DevState S
         g.sync();
         if (trace)
             for (int q = q0 + g.tl; q < q1; q += g.nt) trace[(size_t)(k + 1) * P.nprobe + P.slot[q]] = sv[P.local[q]];
+        if (gs) {  // v_{k+1} of the cell for every partner, then the step's grid barrier
+            double* vn = N.vbuf + (size_t)((k + 1) & 1) * (size_t)G.nnode + pb;
+            for (int i = i0 + g.tl; i < i1; i += g.nt) __stcg(vn + i, sv[i]);
+            if (k + 1 < k1) grid_barrier(N.gbar, N.gerr, G.npack, N.gspin, nact, gen);
+        }
     }
     if (write_tape) {
         const size_t off = (size_t)(k1 - T.k_base) * (size_t)G.nnode + pb;
@@ -266,7 +283,7 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_kernel(DevGroup G, DevState S
     }
     double* vdst = kCpl ? N.vout : S.v;
     for (int i = i0 + g.tl; i < i1; i += g.nt) {
-        vdst[pb + i] = sv[i];
+        if (!gs) vdst[pb + i] = sv[i];  // (grid-synchronous: stored with the last step)
         if ((M.flag[i] & kHasHH) && k1 > k0) {  // gates of step k1 (the update the last step deferred)
             const double gm = S.m[pb + i], gh = S.h[pb + i], gn = S.n[pb + i];
             HHRates rt;
@@ -293,7 +310,9 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_kernel(DevGroup G, DevState S
 // parameters they are (for currents linear in v their v-derivative is 0).
 // Coupled launches (one step): the dL/dv_k contributions of a gap or graded
 // synapse to its partner node go through N.x_*_out and are gathered by the
-// launch of step k-1 from N.x_*_in, in the fixed order of N.node_in.
+// launch of step k-1 from N.x_*_in, in the fixed order of N.node_in.  A
+// grid-synchronous coupled launch (N.gsync) runs many steps: step k writes
+// N.xbuf[k & 1], step k-1 gathers it after the step's grid barrier.
 // kLib: the library mechanisms' state-update adjoints join mu in S + A (their
 // currents recomputed from the tape give d_k and the calcium current), the
 // adjoints of their currents join dL/dv_k in V (hx_lib.cuh).
@@ -327,18 +346,32 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_kernel(DevGroup G, DevTape T,
     double* __restrict__ lmv = Ad.lm + pb;
     double* __restrict__ lhv = Ad.lh + pb;
     double* __restrict__ lnv = Ad.ln + pb;
+    const bool gs = kCpl && N.gsync;
+    // partner contributions to dL/dv_{k+1} written by step k+1 (its launch, or
+    // its iteration of a grid-synchronous launch), in the fixed order of node_in
+    auto gather_in = [&](const double* xhg, const double* xgj, const double* xgr) {
+        for (int i = i0 + g.tl; i < i1; i += g.nt)
+            if (M.flag[i] & kHasIn) {
+                double l = lv[i];
+                const int e1 = __ldg(N.node_in_off + pb + i + 1);
+                for (int e = __ldg(N.node_in_off + pb + i); e < e1; ++e) {
+                    const int code = __ldg(N.node_in + e), kind = code >> 28, inst = code & 0x0FFFFFFF;
+                    l += __ldcg((kind == 0 ? xhg : kind == 1 ? xgj : xgr) + inst);
+                }
+                lv[i] = l;
+            }
+    };
     for (int i = i0 + g.tl; i < i1; i += g.nt) {
         sa[i] = G.a[pb + i];
         sb[i] = G.b[pb + i];
-        if (kCpl && (M.flag[i] & kHasIn)) {  // partner contributions to dL/dv_{k_hi} from the launch of step k_hi
-            double l = lv[i];
-            const int e1 = __ldg(N.node_in_off + pb + i + 1);
-            for (int e = __ldg(N.node_in_off + pb + i); e < e1; ++e) {
-                const int code = __ldg(N.node_in + e), kind = code >> 28, inst = code & 0x0FFFFFFF;
-                l += (kind == 0 ? N.x_hg_in : kind == 1 ? N.x_gj_in : N.x_gr_in)[inst];
-            }
-            lv[i] = l;
-        }
+    }
+    if (kCpl && !gs) gather_in(N.x_hg_in, N.x_gj_in, N.x_gr_in);
+    int nact = 0;
+    unsigned gen = 0;
+    if (gs) {
+        const int s1 = G.pack_slot_off[p + 1] - 1;
+        nact = 32 * (G.cs_warp0[s1] + G.cs_nwarp[s1]);
+        if (threadIdx.x == 0) gen = *(volatile unsigned*)(N.gbar + 1);
     }
     // kNet: the cell's synapses [c0, c1); their adjoints Ad.lA/Ad.lB and
     // gradients are touched only by the thread that owns the synapse's node
@@ -353,6 +386,22 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_kernel(DevGroup G, DevTape T,
     g.sync();
     for (int k = k_hi - 1; k >= k_lo; --k) {
         const size_t off = (size_t)(k - T.k_base) * (size_t)G.nnode + pb;
+        double *xo_hg = nullptr, *xo_gj = nullptr, *xo_gr = nullptr;
+        if (kCpl) {
+            if (gs) {
+                const double* xi = N.xbuf + (size_t)((k + 1) & 1) * N.xstride;
+                double* xo = N.xbuf + (size_t)(k & 1) * N.xstride;
+                gather_in(xi, xi + N.nhg, xi + N.nhg + N.ngj);
+                g.sync();
+                xo_hg = xo;
+                xo_gj = xo + N.nhg;
+                xo_gr = xo + N.nhg + N.ngj;
+            } else {
+                xo_hg = N.x_hg_out;
+                xo_gj = N.x_gj_out;
+                xo_gr = N.x_gr_out;
+            }
+        }
         probe_inject(P, q0, q1, dLdv + (size_t)(k + 1) * P.nprobe, lv, g);
         g.sync();
         const double tm = tmid[k];
@@ -477,7 +526,7 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_kernel(DevGroup G, DevTape T,
                         const double gg = __ldg(N.hg_g + j);
                         GR.hg_g[j] += w * sarea * (vpeer[src] - vk) + ld * sarea;
                         lvn -= w * sarea * gg;
-                        N.x_hg_out[j] = w * sarea * gg;
+                        __stcg(xo_hg + j, w * sarea * gg);
                     }
                     const int j1 = __ldg(N.node_gj_off + gi + 1);
                     for (int j = __ldg(N.node_gj_off + gi); j < j1; ++j) {
@@ -486,7 +535,7 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_kernel(DevGroup G, DevTape T,
                         GR.gj_w[j] += -w * sarea * gg * dv + ld * sarea * gg;
                         GR.gj_g[j] += -w * sarea * ww * dv + ld * sarea * ww;
                         lvn -= w * sarea * ww * gg;
-                        N.x_gj_out[j] = w * sarea * ww * gg;
+                        __stcg(xo_gj + j, w * sarea * ww * gg);
                     }
                     const int r1 = __ldg(N.node_gr_off + gi + 1);
                     for (int j = __ldg(N.node_gr_off + gi); j < r1; ++j) {
@@ -511,7 +560,7 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_kernel(DevGroup G, DevTape T,
                             x = ls * (dinf * (1.0 - E) + (sprev - inf) * dE);
                             ls *= E;
                         }
-                        N.x_gr_out[j] = x;
+                        __stcg(xo_gr + j, x);
                         N.lS[j] = ls;
                     }
                 }
@@ -536,6 +585,7 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_kernel(DevGroup G, DevTape T,
             }
         }
         g.sync();
+        if (gs && k > k_lo) grid_barrier(N.gbar, N.gerr, G.npack, N.gspin, nact, gen);
     }
 }
 
@@ -696,6 +746,9 @@ cudaError_t configure_kernels(size_t smem_fwd, size_t smem_bwd, size_t smem_fwd_
     return cudaFuncSetAttribute(bwd_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_bwd_net);
 }
 
+const void* fwd_cpl_kernel_ptr() { return (const void*)fwd_kernel<true, false, true>; }
+const void* bwd_cpl_kernel_ptr() { return (const void*)bwd_kernel<true, false, true>; }
+
 cudaError_t launch_init(const DevGroup& G, const DevState& S, double v_init, cudaStream_t st) {
     init_state_kernel<<<(G.nnode + 255) / 256, 256, 0, st>>>(G, S, v_init);
     return cudaGetLastError();
@@ -711,6 +764,17 @@ cudaError_t launch_fwd(const DevGroup& G, const DevState& S, const DevTape& T, i
                        double* trace, const double* tmid, int k0, int k1, cudaStream_t st, const DevNet* N,
                        const DevLib* L) {
     if (N) {
+        if (N->coupled && N->gsync) {  // every pack co-resident: one cooperative launch for the window
+            DevGroup Gc = G;
+            DevState Sc = S;
+            DevTape Tc = T;
+            DevProbe Pc = P;
+            DevNet Nc = *N;
+            DevLib Lc{};
+            void* args[] = {&Gc, &Sc, &Tc, &write_tape, &Pc, &trace, &tmid, &k0, &k1, &Nc, &Lc};
+            return cudaLaunchCooperativeKernel((const void*)fwd_kernel<true, false, true>, dim3(G.npack),
+                                               dim3(kThreads), args, fwd_smem_bytes(G), st);
+        }
         if (N->coupled)
             fwd_kernel<true, false, true><<<G.npack, kThreads, fwd_smem_bytes(G), st>>>(G, S, T, write_tape, P, trace,
                                                                                    tmid, k0, k1, *N, DevLib{});
@@ -733,6 +797,18 @@ cudaError_t launch_bwd(const DevGroup& G, const DevTape& T, const DevAdj& A, con
                        const double* dLdv, const double* tmid, int k_hi, int k_lo, cudaStream_t st, const DevNet* N,
                        const DevLib* L) {
     if (N) {
+        if (N->coupled && N->gsync) {
+            DevGroup Gc = G;
+            DevTape Tc = T;
+            DevAdj Ac = A;
+            DevGrad GRc = GR;
+            DevProbe Pc = P;
+            DevNet Nc = *N;
+            DevLib Lc{};
+            void* args[] = {&Gc, &Tc, &Ac, &GRc, &Pc, &dLdv, &tmid, &k_hi, &k_lo, &Nc, &Lc};
+            return cudaLaunchCooperativeKernel((const void*)bwd_kernel<true, false, true>, dim3(G.npack),
+                                               dim3(kThreads), args, bwd_smem_bytes(G), st);
+        }
         if (N->coupled)
             bwd_kernel<true, false, true><<<G.npack, kThreads, bwd_smem_bytes(G), st>>>(G, T, A, GR, P, dLdv, tmid, k_hi,
                                                                                    k_lo, *N, DevLib{});

@@ -12,6 +12,9 @@ size_t bwd_smem_bytes(const DevGroup& G);
 size_t split_fwd_smem_bytes(const DevGroup& G);
 size_t split_bwd_smem_bytes(const DevGroup& G);
 cudaError_t configure_kernels(size_t smem_fwd, size_t smem_bwd, size_t smem_fwd_net, size_t smem_bwd_net);
+// the coupled-network instantiations (occupancy checks of grid-synchronous launches)
+const void* fwd_cpl_kernel_ptr();
+const void* bwd_cpl_kernel_ptr();
 cudaError_t launch_init(const DevGroup& G, const DevState& S, double v_init, cudaStream_t st);
 cudaError_t launch_lib_init(const DevLib& L, int nnode, double v_init, cudaStream_t st);
 // N and L null: the plain kernels; N: the network instantiation; L: the

@@ -199,9 +199,17 @@ int hx_set_tape_budget(hx_ctx* ctx, size_t bytes) {
 
 int hx_set_split_barrier_limit(hx_ctx* ctx, long long sleeps) {
     if (!ctx) return -1;
-    if (sleeps < 0) return fail(ctx, "split barrier limit must be >= 0");
+    if (sleeps < 0) return fail(ctx, "barrier limit must be >= 0");
     ctx->split_spin_limit = sleeps ? sleeps : hx::kSplitSpinLimitDefault;
     ctx->X.spin_limit = ctx->split_spin_limit;
+    ctx->N.gspin = ctx->split_spin_limit;
+    return 0;
+}
+
+int hx_set_grid_sync(hx_ctx* ctx, int enable) {
+    if (!ctx) return -1;
+    ctx->gsync_allowed = enable != 0;
+    ctx->N.gsync = ctx->gsync_fit && ctx->gsync_allowed ? 1 : 0;
     return 0;
 }
 
@@ -371,9 +379,11 @@ int hx_load_group(hx_ctx* ctx, const hx_group_desc* desc) {
         mark(desc->exp2syn_node, desc->nexp2syn, hx::kHasSyn);
         mark(desc->hg_node, desc->nhalfgap, hx::kHasCpl);
         mark(desc->gj_node, desc->ngapj, hx::kHasCpl);
+        mark(desc->gn_node, desc->ngapnp, hx::kHasCpl);
         mark(desc->gr_node, desc->ngraded, hx::kHasCpl);
         mark(desc->hg_src, desc->nhalfgap, hx::kHasIn);
         mark(desc->gj_pre, desc->ngapj, hx::kHasIn);
+        mark(desc->gn_src, desc->ngapnp, hx::kHasIn);
         mark(desc->gr_pre, desc->ngraded, hx::kHasIn);
     }
     HXC(ctx->node_flags.upload(flags, st));
@@ -512,6 +522,19 @@ int hx_load_group(hx_ctx* ctx, const hx_group_desc* desc) {
     HXC(hx::configure_kernels(std::min(hx::fwd_smem_bytes(G), (size_t)maxsmem),
                               std::min(hx::bwd_smem_bytes(G), (size_t)maxsmem), std::min(sfn, (size_t)maxsmem),
                               std::min(sbn, (size_t)maxsmem)));
+    // coupled networks: grid-synchronous launches (many steps a launch, one
+    // grid barrier a step) when every pack can be co-resident
+    ctx->gsync_fit = false;
+    if (ctx->coupled && !ctx->split) {
+        int coop = 0, per_f = 0, per_b = 0;
+        HXC(cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, ctx->device));
+        HXC(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_f, hx::fwd_cpl_kernel_ptr(), hx::kThreads,
+                                                          std::min(sfn, (size_t)maxsmem)));
+        HXC(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_b, hx::bwd_cpl_kernel_ptr(), hx::kThreads,
+                                                          std::min(sbn, (size_t)maxsmem)));
+        ctx->gsync_fit = coop && (long long)std::min(per_f, per_b) * nsm >= P.npack;
+    }
+    ctx->N.gsync = ctx->gsync_fit && ctx->gsync_allowed ? 1 : 0;
     if (ctx->split) {
         if (ctx->net) return fail(ctx, "a cell split across CTAs cannot carry network parts");
         HXC(hx::configure_split(sf, sb));

@@ -64,6 +64,8 @@ int window_from_delay(double dmin, double dt) {
 
 }  // namespace
 
+constexpr int kFreeWindow = 256;
+
 int hx_net_load(hx_ctx* ctx, const hx_group_desc* d) {
     const hx::Plan& P = ctx->P;
     cudaStream_t st = ctx->st;
@@ -296,7 +298,11 @@ int hx_net_load(hx_ctx* ctx, const hx_group_desc* d) {
         return hx_fail(ctx, "NetStim table incomplete");
     ctx->ns_rng = d->netstim_rng;
     ctx->dmin = ns ? dmin : 0.0;
-    ctx->window = ctx->coupled ? 1 : (ns ? window_from_delay(dmin, d->dt) : (1 << 30));
+    // coupled groups without grid-synchronous launches take one step per
+    // window (net_window); without events the window is free and kept at
+    // kFreeWindow steps, so that checkpoint segments (multiples of the
+    // window) can stay near sqrt(nstep)
+    ctx->window = ns ? window_from_delay(dmin, d->dt) : kFreeWindow;
     ctx->ck_net_stride = 2 * (size_t)ns + (size_t)ctx->ngr;
 
     hx::DevNet& N = ctx->N;
@@ -339,13 +345,27 @@ int hx_net_load(hx_ctx* ctx, const hx_group_desc* d) {
     N.coupled = ctx->coupled ? 1 : 0;
     N.node_in_off = ctx->node_in_off.p;
     N.node_in = ctx->node_in.p;
+    N.nhg = ctx->nhg;
+    N.ngj = ctx->ngj;
+    N.vbuf = ctx->vbuf.p;
+    N.xbuf = ctx->xbuf.p;
+    N.xstride = std::max<size_t>((size_t)ctx->nhg + ctx->ngj + ctx->ngr, 1);
+    if (ctx->coupled) {
+        HXC(ctx->gs_bar.ensure(2));
+        HXC(ctx->gs_err.ensure(1));
+        HXC(cudaMemsetAsync(ctx->gs_err.p, 0, 4, st));
+    }
+    N.gbar = ctx->gs_bar.p;
+    N.gerr = ctx->gs_err.p;
+    N.gspin = ctx->split_spin_limit;
+    N.gsync = 0;  // set at load once the packs' co-residency is known
     return 0;
 }
 
 // ---------------------------------------------------------------- forward
 static int net_window(const hx_ctx* c, int nstep) {
     int W = c->window_user > 0 ? c->window_user : c->window;
-    if (c->coupled) W = 1;
+    if (c->coupled && !c->N.gsync) W = 1;
     return std::max(1, std::min(W, std::max(nstep, 1)));
 }
 
@@ -369,7 +389,9 @@ static int net_ck(hx_ctx* ctx, int s, bool save, double* vsrc) {
     return 0;
 }
 
-static int net_plan_tape(hx_ctx* ctx, int nstep, int W) {
+// W: the forward window; a free window (no synapses, no window set by the
+// caller) follows the checkpoint segment instead
+static int net_plan_tape(hx_ctx* ctx, int nstep, int& W) {
     const size_t nn = ctx->P.nnode, ns = ctx->nsyn, ng = ctx->ngr;
     const size_t per_step = (4 * nn + 2 * ns + ng) * sizeof(double);
     size_t budget = ctx->tape_budget;
@@ -396,9 +418,12 @@ static int net_plan_tape(hx_ctx* ctx, int nstep, int W) {
         return alloc((size_t)nstep + 1, 0);
     }
     // segments of K steps, K a multiple of the window
+    const bool free_window = ctx->nsyn == 0 && ctx->window_user <= 0;
+    if (free_window) W = 1;
     size_t K = (size_t)std::sqrt((double)nstep);
     K = std::max<size_t>(W, (K + W - 1) / W * W);
     while (K > (size_t)W && (K + 2 + ((size_t)nstep + K - 1) / K) * per_step > budget) K -= W;
+    if (free_window) W = (int)K;
     if ((K + 2 + ((size_t)nstep + K - 1) / K) * per_step > budget)
         return hx_fail(ctx, "device memory too small for the network tape");
     ctx->full_tape = false;
@@ -442,7 +467,7 @@ int hx_net_forward(hx_ctx* ctx, int nstep, double v_init, double* trace_dev, boo
     cudaStream_t st = ctx->st;
     const hx::Plan& P = ctx->P;
     const size_t nn = P.nnode;
-    const int W = net_window(ctx, nstep);
+    int W = net_window(ctx, nstep);
     const int ncell = (int)P.cs_node0.size();
     // Several ranks exchange window spikes: every rank takes the same
     // collective steps whatever happens locally.  A host-side failure on one
@@ -459,7 +484,7 @@ int hx_net_forward(hx_ctx* ctx, int nstep, double v_init, double* trace_dev, boo
     // most every other step); ranks that exchange send buffers of the agreed
     // size win_cap_cur (most windows carry far fewer spikes than the bound),
     // grown on every rank alike when one overflows
-    const int own_cap = ncell * ((W + 1) / 2) + 1;
+    int own_cap = 0;  // (W is final after the tape plan below)
     const size_t nbucket = (size_t)std::max(nstep, 1) * (size_t)std::max(P.npack, 1);  // (step, pack) event buckets
     if (multi) {
         HXC(ctx->st_send.ensure(2));
@@ -477,6 +502,8 @@ int hx_net_forward(hx_ctx* ctx, int nstep, double v_init, double* trace_dev, boo
     };
     bool ok = setup() == 0;
     if (!ok && !multi) return -1;
+    if (ctx->coupled && !ctx->N.gsync) W = 1;
+    own_cap = ncell * ((W + 1) / 2) + 1;
     std::string local_err = ok ? std::string() : ctx->err;
     hx::DevProbe PV = hx_probe_view(ctx);
     const double half_dt = ctx->dt / 2;
@@ -496,6 +523,7 @@ int hx_net_forward(hx_ctx* ctx, int nstep, double v_init, double* trace_dev, boo
             HXC(cudaMemsetAsync(ctx->win_max.p, 0, 4, st));
             HXC(cudaMemsetAsync(ctx->log_n.p, 0, 4, st));
             HXC(cudaMemsetAsync(ctx->cs_ps_flag.p, 0, (size_t)std::max(ncell, 1) * 4, st));
+            if (ctx->N.gsync) HXC(cudaMemsetAsync(ctx->gs_err.p, 0, 4, st));
             double* v0 = ctx->coupled ? ctx->vbuf.p : ctx->sv.p;
             HXC(hx::launch_init(ctx->G, hx::DevState{v0, ctx->sm.p, ctx->sh.p, ctx->sn.p}, v_init, st));
             HXC(hx::launch_init_net(ctx->nsyn, ctx->sA.p, ctx->sB.p, ctx->ngr, ctx->prm[HX_P_GRADED_W].p,
@@ -533,6 +561,10 @@ int hx_net_forward(hx_ctx* ctx, int nstep, double v_init, double* trace_dev, boo
                 N.tB = ctx->tB.p;
                 N.tS = ctx->tS.p;
                 write_tape = 1;
+            }
+            if (N.gsync) {
+                N.vout = ctx->vbuf.p + (size_t)(k1 & 1) * nn;  // stored by the last step
+                HXC(cudaMemsetAsync(ctx->gs_bar.p, 0, 2 * sizeof(unsigned), st));
             }
             hx::DevState S{vin, ctx->sm.p, ctx->sh.p, ctx->sn.p};
             HXC(hx::launch_fwd(ctx->G, S, T, write_tape, PV, trace_dev, ctx->tmid.p, k0, k1, st, &N));
@@ -604,7 +636,10 @@ int hx_net_forward(hx_ctx* ctx, int nstep, double v_init, double* trace_dev, boo
         } else {
             HXC(cudaEventRecord(ctx->ev[1], st));
             HXC(cudaMemcpyAsync(&err, ctx->dev_err.p, 4, cudaMemcpyDeviceToHost, st));
+            int gerr = 0;
+            if (ctx->N.gsync) HXC(cudaMemcpyAsync(&gerr, ctx->gs_err.p, 4, cudaMemcpyDeviceToHost, st));
             HXC(cudaStreamSynchronize(st));
+            if (gerr) return hx_fail(ctx, "a grid barrier of the coupled-network kernels timed out");
         }
         ctx->launches[0] = launches + (multi ? 1 : 0);
         if (err & HX_XS_LATE_EVENT)
@@ -645,6 +680,8 @@ int hx_net_backward(hx_ctx* ctx, const double* dLdv_dev) {
     }
     if (ctx->ngr) HXC(cudaMemsetAsync(ctx->lS.p, 0, (size_t)ctx->ngr * 8, st));
     if (ctx->coupled) HXC(cudaMemsetAsync(ctx->xbuf.p, 0, 2 * std::max<size_t>(nx, 1) * 8, st));
+    const bool gsync = ctx->coupled && ctx->N.gsync;
+    if (gsync) HXC(cudaMemsetAsync(ctx->gs_err.p, 0, 4, st));
     HXC(cudaMemsetAsync(ctx->grad.p, 0, ctx->grad_off[HX_P_COUNT] * 8, st));
     double* g = ctx->grad.p;
     hx::DevGrad GR{g + ctx->grad_off[HX_P_HH_GNABAR], g + ctx->grad_off[HX_P_HH_GKBAR], g + ctx->grad_off[HX_P_HH_GL],
@@ -676,7 +713,8 @@ int hx_net_backward(hx_ctx* ctx, const double* dLdv_dev) {
     };
     auto sweep = [&](int k_hi, int k_lo, const hx::DevTape& T) -> int {
         if (hx_kev_mark(ctx, st)) return -1;
-        if (!ctx->coupled) {
+        if (!ctx->coupled || gsync) {
+            if (gsync) HXC(cudaMemsetAsync(ctx->gs_bar.p, 0, 2 * sizeof(unsigned), st));
             HXC(hx::launch_bwd(ctx->G, T, A, GR, PV, dLdv_dev, ctx->tmid.p, k_hi, k_lo, st, &N));
         } else {
             for (int k = k_hi - 1; k >= k_lo; --k) {
@@ -685,7 +723,7 @@ int hx_net_backward(hx_ctx* ctx, const double* dLdv_dev) {
             }
         }
         if (hx_kev_mark(ctx, st)) return -1;
-        return ctx->coupled ? k_hi - k_lo : 1;
+        return ctx->coupled && !gsync ? k_hi - k_lo : 1;
     };
     HXC(cudaEventRecord(ctx->ev[2], st));
     ctx->kev_n = 0;
@@ -703,6 +741,16 @@ int hx_net_backward(hx_ctx* ctx, const double* dLdv_dev) {
                 if (net_ck(ctx, s, false, ctx->sv.p)) return -1;
                 hx::DevState S{ctx->sv.p, ctx->sm.p, ctx->sh.p, ctx->sn.p};
                 HXC(hx::launch_fwd(ctx->G, S, T, 1, PV, nullptr, ctx->tmid.p, k0, k1, st, &N));
+                launches++;
+            } else if (gsync) {  // the segment's recompute in one grid-synchronous launch
+                double* vin = ctx->vbuf.p + (size_t)(k0 & 1) * nn;
+                if (net_ck(ctx, s, false, vin)) return -1;
+                hx::DevNet NF = N;
+                NF.vpeer = vin;
+                NF.vout = ctx->vbuf.p + (size_t)(k1 & 1) * nn;
+                hx::DevState S{vin, ctx->sm.p, ctx->sh.p, ctx->sn.p};
+                HXC(cudaMemsetAsync(ctx->gs_bar.p, 0, 2 * sizeof(unsigned), st));
+                HXC(hx::launch_fwd(ctx->G, S, T, 1, PV, nullptr, ctx->tmid.p, k0, k1, st, &NF));
                 launches++;
             } else {
                 if (net_ck(ctx, s, false, ctx->vbuf.p + (size_t)(k0 & 1) * nn)) return -1;
@@ -722,6 +770,12 @@ int hx_net_backward(hx_ctx* ctx, const double* dLdv_dev) {
     }
     HXC(cudaEventRecord(ctx->ev[3], st));
     ctx->launches[1] = launches;
+    if (gsync) {
+        int gerr = 0;
+        HXC(cudaMemcpyAsync(&gerr, ctx->gs_err.p, 4, cudaMemcpyDeviceToHost, st));
+        HXC(cudaStreamSynchronize(st));
+        if (gerr) return hx_fail(ctx, "a grid barrier of the coupled-network kernels timed out");
+    }
     return 0;
 }
 
@@ -826,7 +880,7 @@ int hx_get_window(hx_ctx* ctx, int* steps) {
     if (!ctx || !steps) return -1;
     if (!ctx->loaded) return hx_fail(ctx, "no group loaded");
     *steps = ctx->window_user > 0 ? ctx->window_user : ctx->window;
-    if (ctx->coupled) *steps = 1;
+    if (ctx->coupled && !ctx->N.gsync) *steps = 1;
     return 0;
 }
 

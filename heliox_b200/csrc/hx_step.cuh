@@ -152,6 +152,42 @@ struct Grp {
     }
 };
 
+// Grid barrier of a grid-synchronous coupled launch over the CTA's active
+// threads (nact: the pack's warps x 32; idle warps have returned): named
+// barrier 15 (cell groups use 1..8), then thread 0 arrives at the grid
+// counter and waits for the generation to move.  Every wait is bounded: a
+// wait that gives up sets *err, and later barriers return at once (the
+// launch then finishes its loop and the host reports the error).
+__device__ __forceinline__ void grid_barrier(unsigned* bar, int* err, int nblocks, long long spin, int nact,
+                                             unsigned& gen) {
+    asm volatile("bar.sync 15, %0;" ::"r"(nact) : "memory");
+    if (threadIdx.x == 0) {
+        volatile unsigned* vgen = bar + 1;
+        volatile int* verr = err;
+        __threadfence();
+        if (*verr == 0) {
+            const unsigned arrived = atomicAdd(bar, 1u);
+            if (arrived == (unsigned)nblocks - 1u) {
+                atomicExch(bar, 0u);
+                __threadfence();
+                atomicAdd(bar + 1, 1u);
+            } else {
+                long long it = 0;
+                while (*vgen == gen && *verr == 0) {
+                    if (++it > spin) {
+                        atomicOr(err, 1);
+                        break;
+                    }
+                    __nanosleep(100);
+                }
+            }
+        }
+        __threadfence();
+        gen++;
+    }
+    asm volatile("bar.sync 15, %0;" ::"r"(nact) : "memory");
+}
+
 // Bytes of the Meta tables in shared memory (a multiple of 16).
 __host__ __device__ inline size_t meta_bytes(const DevGroup& G) {
     const size_t ints = 4 * (size_t)G.smem_br + 1 + 2 * (size_t)G.smem_bch + G.smem_lvl;
@@ -507,7 +543,7 @@ __device__ __forceinline__ void load_syn(const DevNet& N, const SynNext& nx, con
 template <bool kCpl>
 __device__ __forceinline__ void assemble_net(const DevGroup& G, const DevNet& N, int gi, int fl, double vi,
                                              const double* __restrict__ synA, const double* __restrict__ synB,
-                                             const SynPre& sp, const double* __restrict__ grs,
+                                             const SynPre& sp, const double* grs,
                                              const double* __restrict__ vpeer, double& r, double& dd) {
     if (!(fl & (kHasSyn | kHasCpl))) return;
     const double sarea = sp.sarea;
@@ -523,12 +559,14 @@ __device__ __forceinline__ void assemble_net(const DevGroup& G, const DevNet& N,
     if (!kCpl || !(fl & kHasCpl)) return;
     const int h1 = __ldg(N.node_hg_off + gi + 1);
     for (int j = __ldg(N.node_hg_off + gi); j < h1; ++j) {
-        const double vg = vpeer[__ldg(N.hg_src + j)], g = __ldg(N.hg_g + j);
+        // partner voltages with L2-coherent loads: a grid-synchronous launch
+        // rewrites vpeer's buffer between steps
+        const double vg = __ldcg(vpeer + __ldg(N.hg_src + j)), g = __ldg(N.hg_g + j);
         pp_add((vg - (vi + kFdEps)) * g, (vg - vi) * g, sarea, true, r, dd);
     }
     const int j1 = __ldg(N.node_gj_off + gi + 1);
     for (int j = __ldg(N.node_gj_off + gi); j < j1; ++j) {
-        const double vp = vpeer[__ldg(N.gj_pre + j)], g = __ldg(N.gj_g + j), w = __ldg(N.gj_w + j);
+        const double vp = __ldcg(vpeer + __ldg(N.gj_pre + j)), g = __ldg(N.gj_g + j), w = __ldg(N.gj_w + j);
         pp_add(w * (g * ((vi + kFdEps) - vp)), w * (g * (vi - vp)), sarea, false, r, dd);
     }
     const int r1 = __ldg(N.node_gr_off + gi + 1);

@@ -199,6 +199,10 @@ class Sim:
         """Bound of a split-cell grid-barrier wait, in ~100 ns sleeps (0 = default, ~2 s)."""
         self._check(self._L.hx_set_split_barrier_limit(self._ctx, int(sleeps)), "hx_set_split_barrier_limit")
 
+    def set_grid_sync(self, enable: bool = True):
+        """Coupled groups: many steps a launch with a grid barrier per step (True, when the packs fit) or one launch per step."""
+        self._check(self._L.hx_set_grid_sync(self._ctx, 1 if enable else 0), "hx_set_grid_sync")
+
     def set_window(self, steps: int):
         self._check(self._L.hx_set_window(self._ctx, int(steps)), "hx_set_window")
 

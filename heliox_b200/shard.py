@@ -109,10 +109,11 @@ def shard(g: CellGroup, nranks: int, rank: int) -> Tuple[CellGroup, int, int]:
 
 def window_of(g: CellGroup) -> int:
     """Steps per forward window of an event network: no longer than the
-    smallest NetCon delay (the rule the library applies to one group)."""
+    smallest NetCon delay (the rule the library applies to one group);
+    without synapses the window is free and the library keeps it at 256."""
     d = np.concatenate([g.expsyn.fields["delay"], g.exp2syn.fields["delay"]])
     if d.size == 0:
-        return 1 << 30
+        return 256
     lag = np.floor((d.min() - 0.5 * g.dt) / g.dt) - 1.0
     return int(max(1.0, lag))
 

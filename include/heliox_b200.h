@@ -309,15 +309,23 @@ int hx_set_pack_target(hx_ctx* ctx, int nodes_per_warp);
  * does not fit, the backward recomputes checkpointed segments.  0 = default
  * (60% of free device memory at load time). */
 int hx_set_tape_budget(hx_ctx* ctx, size_t bytes);
-/* How long a grid-barrier wait of the split-cell kernels (a cell larger than
- * one CTA) lasts before it gives up: `sleeps` waits of ~100 ns (0 = default,
- * 20,000,000: ~2 s).  A wait that gives up sets an error flag, later barriers
- * return at once, the launch finishes, and the forward or backward returns -1
- * with "a grid barrier of the split-cell kernels timed out"; the context stays
- * usable.  Takes effect at the next launch.  (The reference's intra-cell
- * parallel solvers synchronise inside one kernel, simulate.cu:119-189; this
- * bounds the cross-CTA form.) */
+/* How long a grid-barrier wait lasts before it gives up -- the split-cell
+ * kernels (a cell larger than one CTA) and the grid-synchronous launches of
+ * coupled networks: `sleeps` waits of ~100 ns (0 = default, 20,000,000:
+ * ~2 s).  A wait that gives up sets an error flag, later barriers return at
+ * once, the launch finishes, and the forward or backward returns -1 with "a
+ * grid barrier of the ... kernels timed out"; the context stays usable.
+ * Takes effect at the next launch.  (The reference's intra-cell parallel
+ * solvers synchronise inside one kernel, simulate.cu:119-189; this bounds the
+ * cross-CTA form.) */
 int hx_set_split_barrier_limit(hx_ctx* ctx, long long sleeps);
+/* Groups coupled by gap junctions or graded synapses exchange voltages every
+ * step.  enable = 1 (default): when every cell pack can be co-resident, a
+ * launch runs a whole window of steps with one grid barrier per step
+ * (cooperative launch); 0: one launch per step.  Results are identical.
+ * (Replaces the per-step gap transfer of simulate.cpp:953-966 between
+ * mechanism launches.) */
+int hx_set_grid_sync(hx_ctx* ctx, int enable);
 
 /* ---- model ---------------------------------------------------------------- */
 /* Replaces SimRuntimeCore::load_model -> read_coredat -> data_format_trans

@@ -163,3 +163,56 @@ def test_gapjunction_noptr_forward_and_gradients(Sim):
     ref2, _ = O.forward(g2, 600, probe=p)
     _check_v(tr2, ref2)
     s.close()
+
+
+def _coupled_run(Sim, g, T, grid_sync, tape_budget=0, probes=None):
+    s = Sim(0, tape_budget_bytes=tape_budget)
+    s.load_group(g)
+    s.set_grid_sync(grid_sync)
+    p = g.soma_nodes() if probes is None else probes
+    c = np.random.default_rng(7).standard_normal((T + 1, p.shape[0]))
+    tr = s.forward_capture(T, probes=p)
+    gg = s.backward(c)
+    window = s.window()
+    s.close()
+    return tr, gg, window
+
+
+@pytest.mark.parametrize("tape_budget", [0, 16 << 20])
+def test_coupled_grid_sync_equals_per_step_launches(Sim, tape_budget):
+    """Coupled groups run whole windows in one cooperative launch with a grid
+    barrier per step (forward, checkpoint recompute and reverse sweep); the
+    traces and every gradient equal those of one launch per step bit for bit,
+    and the oracle's within tolerance."""
+    g = synth.coupled_network(ncell=40, seed=12, ngap=60, ngapj=10, ngraded=80, ngapnp=10)
+    T = 800
+    tr1, g1, w1 = _coupled_run(Sim, g, T, True, tape_budget)
+    tr0, g0, w0 = _coupled_run(Sim, g, T, False, tape_budget)
+    assert w0 == 1 and w1 > 1  # the grid-synchronous launch runs many steps
+    assert np.array_equal(tr1, tr0)
+    for k in g0:
+        assert np.array_equal(g1[k], g0[k]), k
+    ref, gr = O.adjoint(g, T, np.random.default_rng(7).standard_normal((T + 1, g.ncell)))
+    _check_v(tr1, ref)
+    _check_g(g1, gr, GRAD_KINDS + NET_KINDS + ("gapjunction_noptr.weight",))
+
+
+def test_coupled_grid_barrier_wait_gives_up_and_context_recovers(Sim):
+    """A grid-barrier wait of the coupled launches bounded to one ~100 ns sleep
+    runs out (40 CTAs never all arrive within it at every step of 400): the
+    forward reports the timeout instead of waiting; with the default bound the
+    same context runs the forward to the oracle's trace."""
+    from heliox_b200.runtime import HxError
+
+    g = synth.coupled_network(ncell=40, seed=13, ngap=60, ngapj=0, ngraded=80)
+    s = Sim(0)
+    s.load_group(g)
+    assert s.plan_stats()["npack"] >= 8
+    s.set_split_barrier_limit(1)
+    with pytest.raises(HxError, match="timed out"):
+        s.simulate(400)
+    s.set_split_barrier_limit(0)
+    tr = s.simulate(400)
+    ref, _ = O.forward(g, 400)
+    _check_v(tr, ref)
+    s.close()
