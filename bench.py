@@ -317,6 +317,7 @@ def run_ours(args):
     del tsim
 
     s = new_sim(g)
+    s.set_grad_kinds(keys)  # the workload's gradients only (the reverse sweep skips the other accumulators)
     target = torch.from_numpy(target_h).to(dev)
     trace = torch.empty_like(target)
     dLdv = torch.empty_like(target)

@@ -172,6 +172,7 @@ SIGNATURES = {
     "hx_set_tape_budget": (C.c_int, [C.c_void_p, C.c_size_t]),
     "hx_set_split_barrier_limit": (C.c_int, [C.c_void_p, C.c_longlong]),
     "hx_set_grid_sync": (C.c_int, [C.c_void_p, C.c_int]),
+    "hx_set_grad_kinds": (C.c_int, [C.c_void_p, _ip, C.c_int]),
     "hx_load_group": (C.c_int, [C.c_void_p, C.POINTER(GroupDesc)]),
     "hx_get_plan_stats": (C.c_int, [C.c_void_p, C.POINTER(PlanStats)]),
     "hx_plan_check": (C.c_int, [C.POINTER(GroupDesc), C.c_int, C.POINTER(PlanStats), _dp, _dp]),

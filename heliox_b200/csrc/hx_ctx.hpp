@@ -82,6 +82,7 @@ struct hx_ctx {
     int pack_target = 0;
     size_t tape_budget = 0;
     long long split_spin_limit = hx::kSplitSpinLimitDefault;
+    unsigned grad_skip = 0;  // DevGrad::skip of the next backward (hx_set_grad_kinds)
     bool loaded = false;
     hx::Plan P;
     double dt = 0.025, celsius = 6.3;

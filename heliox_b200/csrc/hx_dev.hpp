@@ -69,6 +69,10 @@ struct DevGrad {
     double *pas_g, *pas_e, *cm, *ic_amp;
     double *syn_w, *syn_e;             // exponential synapses (ExpSyn then Exp2Syn per node)
     double *hg_g, *gj_g, *gj_w, *gr_w;  // HalfGap, gapjunction_lr, neuron_to_neuron_syn_lr
+    // accumulators the caller did not ask for (bit 1 << HX_P_* kind, kinds
+    // 0..15): neither read nor written, so the reverse sweep moves only the
+    // requested gradients
+    unsigned skip;
 };
 
 // A cell split across CTAs (hx_plan.hpp): pack 0 holds the top part, the

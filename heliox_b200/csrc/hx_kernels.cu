@@ -480,7 +480,7 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_kernel(DevGroup G, DevTape T,
                 if (sp.s0 < sp.s1) {
                     la0 = slA[sp.s0];
                     lb0 = slB[sp.s0];
-                    ge0 = GR.syn_e[sp.s0];
+                    if (!(GR.skip & (1u << HX_P_EXPSYN_E))) ge0 = GR.syn_e[sp.s0];
                 }
             }
             const double w = sw[i];
@@ -508,14 +508,15 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_kernel(DevGroup G, DevTape T,
                     double Gs = sp.B0 - sp.A0, lG = sarea * (ld - w * (vk - sp.E0));
                     slB[sp.s0] = lb0 + lG;
                     slA[sp.s0] = la0 - lG;
-                    GR.syn_e[sp.s0] = ge0 + w * sarea * Gs;
+                    const bool g_e = !(GR.skip & (1u << HX_P_EXPSYN_E));
+                    if (g_e) GR.syn_e[sp.s0] = ge0 + w * sarea * Gs;
                     lvn -= w * sarea * Gs;
                     for (int j = sp.s0 + 1; j < sp.s1; ++j) {
                         Gs = tB[j] - tA[j];
                         lG = sarea * (ld - w * (vk - __ldg(N.syn_e + j)));
                         slB[j] += lG;
                         slA[j] -= lG;
-                        GR.syn_e[j] += w * sarea * Gs;
+                        if (g_e) GR.syn_e[j] += w * sarea * Gs;
                         lvn -= w * sarea * Gs;
                     }
                 }
@@ -524,7 +525,7 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_kernel(DevGroup G, DevTape T,
                     for (int j = __ldg(N.node_hg_off + gi); j < h1; ++j) {
                         const int src = __ldg(N.hg_src + j);
                         const double gg = __ldg(N.hg_g + j);
-                        GR.hg_g[j] += w * sarea * (vpeer[src] - vk) + ld * sarea;
+                        if (!(GR.skip & (1u << HX_P_HALFGAP_G))) GR.hg_g[j] += w * sarea * (vpeer[src] - vk) + ld * sarea;
                         lvn -= w * sarea * gg;
                         __stcg(xo_hg + j, w * sarea * gg);
                     }
@@ -532,8 +533,8 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_kernel(DevGroup G, DevTape T,
                     for (int j = __ldg(N.node_gj_off + gi); j < j1; ++j) {
                         const int q = __ldg(N.gj_pre + j);
                         const double gg = __ldg(N.gj_g + j), ww = __ldg(N.gj_w + j), dv = vk - vpeer[q];
-                        GR.gj_w[j] += -w * sarea * gg * dv + ld * sarea * gg;
-                        GR.gj_g[j] += -w * sarea * ww * dv + ld * sarea * ww;
+                        if (!(GR.skip & (1u << HX_P_GAPJ_W))) GR.gj_w[j] += -w * sarea * gg * dv + ld * sarea * gg;
+                        if (!(GR.skip & (1u << HX_P_GAPJ_G))) GR.gj_g[j] += -w * sarea * ww * dv + ld * sarea * ww;
                         lvn -= w * sarea * ww * gg;
                         __stcg(xo_gj + j, w * sarea * ww * gg);
                     }
@@ -543,7 +544,8 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_kernel(DevGroup G, DevTape T,
                         const double er = __ldg(N.gr_erev + j), sk = grs[j], dvr = vk - er;
                         double ls = N.lS[j] - w * sarea * aw * gg * dvr + ld * sarea * aw * gg;
                         const double sgn = (double)((W > 0) - (W < 0));
-                        GR.gr_w[j] += sgn * (-w * sarea * gg * sk * dvr + ld * sarea * gg * sk);
+                        if (!(GR.skip & (1u << HX_P_GRADED_W)))
+                            GR.gr_w[j] += sgn * (-w * sarea * gg * sk * dvr + ld * sarea * gg * sk);
                         lvn -= w * sarea * aw * gg * sk;
                         // state map s_k = F(s_{k-1}, vpre_k): its vpre_k part goes to the
                         // presynaptic node (gathered by the launch of step k-1)
@@ -574,7 +576,7 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_kernel(DevGroup G, DevTape T,
             }
             lv[i] = lvn;
         }
-        if (kNet) {  // event weight gradients: dL/dw += fA lA' + fB lB' per delivery at step k (owner thread)
+        if (kNet && !(GR.skip & (1u << HX_P_EXPSYN_W))) {  // event weight gradients: dL/dw += fA lA' + fB lB' per delivery at step k (owner thread)
             const size_t b = (size_t)k * N.npack + p;
             const int cnt = min(ev_k, N.ev_cap);
             const int* ev = N.ev_syn + b * N.ev_cap;

@@ -206,6 +206,23 @@ int hx_set_split_barrier_limit(hx_ctx* ctx, long long sleeps) {
     return 0;
 }
 
+int hx_set_grad_kinds(hx_ctx* ctx, const int* kinds, int n) {
+    if (!ctx) return -1;
+    if (n <= 0) {
+        ctx->grad_skip = 0;
+        return 0;
+    }
+    if (!kinds) return fail(ctx, "null kinds");
+    unsigned need = 0;
+    for (int i = 0; i < n; i++) {
+        if (kinds[i] < 0 || kinds[i] >= HX_P_COUNT) return fail(ctx, "bad parameter kind");
+        const int sk = store_kind(kinds[i]);
+        if (sk < 16) need |= 1u << sk;
+    }
+    ctx->grad_skip = ~need & 0xFFFFu;
+    return 0;
+}
+
 int hx_set_grid_sync(hx_ctx* ctx, int enable) {
     if (!ctx) return -1;
     ctx->gsync_allowed = enable != 0;
@@ -867,6 +884,7 @@ static int run_backward(hx_ctx* ctx, const double* dLdv_dev) {
     hx::DevGrad GR{g + ctx->grad_off[HX_P_HH_GNABAR], g + ctx->grad_off[HX_P_HH_GKBAR], g + ctx->grad_off[HX_P_HH_GL],
                    g + ctx->grad_off[HX_P_HH_EL],     g + ctx->grad_off[HX_P_PAS_G],   g + ctx->grad_off[HX_P_PAS_E],
                    g + ctx->grad_off[HX_P_CM],        g + ctx->grad_off[HX_P_IC_AMP]};
+    GR.skip = ctx->grad_skip;
     hx::DevProbe PV = hx_probe_view(ctx);
     hx::DevState S = state_view(ctx);
     if (ctx->split) HXC(cudaMemsetAsync(ctx->split_err.p, 0, 4, ctx->st));

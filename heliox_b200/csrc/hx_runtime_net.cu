@@ -689,6 +689,7 @@ int hx_net_backward(hx_ctx* ctx, const double* dLdv_dev) {
                    g + ctx->grad_off[HX_P_CM],        g + ctx->grad_off[HX_P_IC_AMP],  g + ctx->grad_off[HX_P_EXPSYN_W],
                    g + ctx->grad_off[HX_P_EXPSYN_E],  g + ctx->grad_off[HX_P_HALFGAP_G], g + ctx->grad_off[HX_P_GAPJ_G],
                    g + ctx->grad_off[HX_P_GAPJ_W],    g + ctx->grad_off[HX_P_GRADED_W]};
+    GR.skip = ctx->grad_skip;
     hx::DevAdj A{ctx->lv.p, ctx->lm.p, ctx->lh.p, ctx->ln.p, ctx->lA.p, ctx->lB.p};
     hx::DevProbe PV = hx_probe_view(ctx);
     hx::DevNet N = ctx->N;

@@ -5,6 +5,7 @@
 
 #include <cuda_runtime.h>
 
+#include "heliox_b200.h"
 #include "hx_dev.hpp"
 #include "hx_lib.cuh"
 #include "hx_mech.cuh"
@@ -637,26 +638,32 @@ __device__ __forceinline__ double gate_adj(double v1, double q10, double dt, dou
 __device__ __forceinline__ double vjp_mech(const DevGroup& G, const DevGrad& GR, const DevTape& T, size_t off, int i,
                                            int gi, int fl, const NodePar& q, double w, double vk, double ld,
                                            double tm, double lvn, double& lm, double& lh, double& ln) {
+    // accumulators the caller asked for (GR.skip clear), all loaded before the first store
+    const unsigned sk = GR.skip;
+    const bool g_pg = !(sk & (1u << HX_P_PAS_G)), g_pe = !(sk & (1u << HX_P_PAS_E));
+    const bool g_na = !(sk & (1u << HX_P_HH_GNABAR)), g_k = !(sk & (1u << HX_P_HH_GKBAR));
+    const bool g_l = !(sk & (1u << HX_P_HH_GL)), g_el = !(sk & (1u << HX_P_HH_EL));
+    const bool g_cm = !(sk & (1u << HX_P_CM)), g_ic = !(sk & (1u << HX_P_IC_AMP));
     double m = 0.0, h = 0.0, nn = 0.0;
-    double a_pg = 0.0, a_pe = 0.0, a_na = 0.0, a_k = 0.0, a_l = 0.0, a_el = 0.0;
+    double a_pg = 0.0, a_pe = 0.0, a_na = 0.0, a_k = 0.0, a_l = 0.0, a_el = 0.0, a_cm = 0.0;
     if (fl & kHasPas) {
-        a_pg = GR.pas_g[gi];
-        a_pe = GR.pas_e[gi];
+        if (g_pg) a_pg = GR.pas_g[gi];
+        if (g_pe) a_pe = GR.pas_e[gi];
     }
     if (fl & kHasHH) {
         // the gates' last read of their tape row (streaming loads)
         m = __ldcs(T.m + off + i);
         h = __ldcs(T.h + off + i);
         nn = __ldcs(T.n + off + i);
-        a_na = GR.hh_gnabar[gi];
-        a_k = GR.hh_gkbar[gi];
-        a_l = GR.hh_gl[gi];
-        a_el = GR.hh_el[gi];
+        if (g_na) a_na = GR.hh_gnabar[gi];
+        if (g_k) a_k = GR.hh_gkbar[gi];
+        if (g_l) a_l = GR.hh_gl[gi];
+        if (g_el) a_el = GR.hh_el[gi];
     }
-    const double a_cm = GR.cm[gi];
+    if (g_cm) a_cm = GR.cm[gi];
     if (fl & kHasPas) {
-        GR.pas_g[gi] = a_pg + (ld - w * (vk - q.pas_e));
-        GR.pas_e[gi] = a_pe + w * q.pas_g;
+        if (g_pg) GR.pas_g[gi] = a_pg + (ld - w * (vk - q.pas_e));
+        if (g_pe) GR.pas_e[gi] = a_pe + w * q.pas_g;
         lvn -= w * q.pas_g;
     }
     if (fl & kHasHH) {
@@ -664,21 +671,22 @@ __device__ __forceinline__ double vjp_mech(const DevGroup& G, const DevGrad& GR,
         const double t_k = ld - w * (vk - q.ek);
         const double t_l = ld - w * (vk - q.el);
         const double m2h = m * m * h, n3 = nn * nn * nn;
-        GR.hh_gnabar[gi] = a_na + m2h * m * t_na;
-        GR.hh_gkbar[gi] = a_k + n3 * nn * t_k;
-        GR.hh_gl[gi] = a_l + t_l;
-        GR.hh_el[gi] = a_el + w * q.gl;
+        if (g_na) GR.hh_gnabar[gi] = a_na + m2h * m * t_na;
+        if (g_k) GR.hh_gkbar[gi] = a_k + n3 * nn * t_k;
+        if (g_l) GR.hh_gl[gi] = a_l + t_l;
+        if (g_el) GR.hh_el[gi] = a_el + w * q.gl;
         lm += 3.0 * q.gnabar * m2h * t_na;
         lh += q.gnabar * m * m * m * t_na;
         ln += 4.0 * q.gkbar * n3 * t_k;
         lvn -= w * (q.gnabar * m2h * m + q.gkbar * n3 * nn + q.gl);
     }
-    for (int k2 = q.ic0; k2 < q.ic1; ++k2) {
-        const int j = __ldg(G.node_ic + k2);
-        const double del = __ldg(G.ic_del + j), dur = __ldg(G.ic_dur + j);
-        if (tm < del + dur && tm >= del) GR.ic_amp[j] += w * (1.e2 / __ldg(G.area + gi));
-    }
-    GR.cm[gi] = a_cm + ld * G.cfac;
+    if (g_ic)
+        for (int k2 = q.ic0; k2 < q.ic1; ++k2) {
+            const int j = __ldg(G.node_ic + k2);
+            const double del = __ldg(G.ic_del + j), dur = __ldg(G.ic_dur + j);
+            if (tm < del + dur && tm >= del) GR.ic_amp[j] += w * (1.e2 / __ldg(G.area + gi));
+        }
+    if (g_cm) GR.cm[gi] = a_cm + ld * G.cfac;
     return lvn;
 }
 

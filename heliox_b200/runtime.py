@@ -199,6 +199,14 @@ class Sim:
         """Bound of a split-cell grid-barrier wait, in ~100 ns sleeps (0 = default, ~2 s)."""
         self._check(self._L.hx_set_split_barrier_limit(self._ctx, int(sleeps)), "hx_set_split_barrier_limit")
 
+    def set_grad_kinds(self, keys=None):
+        """Accumulate only these gradient kinds in the next backward passes (None: all); the others read as zero."""
+        if not keys:
+            self._check(self._L.hx_set_grad_kinds(self._ctx, None, 0), "hx_set_grad_kinds")
+            return
+        k = np.array([_lib.HX_P[key] for key in keys], dtype=np.int32)
+        self._check(self._L.hx_set_grad_kinds(self._ctx, _lib.iptr(k), int(k.shape[0])), "hx_set_grad_kinds")
+
     def set_grid_sync(self, enable: bool = True):
         """Coupled groups: many steps a launch with a grid barrier per step (True, when the packs fit) or one launch per step."""
         self._check(self._L.hx_set_grid_sync(self._ctx, 1 if enable else 0), "hx_set_grid_sync")

@@ -319,6 +319,14 @@ int hx_set_tape_budget(hx_ctx* ctx, size_t bytes);
  * solvers synchronise inside one kernel, simulate.cu:119-189; this bounds the
  * cross-CTA form.) */
 int hx_set_split_barrier_limit(hx_ctx* ctx, long long sleeps);
+/* The parameter kinds whose gradients the next backward passes accumulate
+ * (n <= 0: all kinds, the default).  The reverse sweep then neither reads nor
+ * writes the accumulators of the other cell and network kinds (library kinds
+ * are always accumulated), and their gradients read as zero -- through
+ * hx_backward, hx_reduce_grads_f32 or an optimizer alike.  Persists until
+ * changed.  (The reference's replay computes only the requested handles'
+ * columns, LearnRuntime.h:72-100.) */
+int hx_set_grad_kinds(hx_ctx* ctx, const int* kinds, int n);
 /* Groups coupled by gap junctions or graded synapses exchange voltages every
  * step.  enable = 1 (default): when every cell pack can be co-resident, a
  * launch runs a whole window of steps with one grid barrier per step

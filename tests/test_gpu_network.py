@@ -216,3 +216,32 @@ def test_coupled_grid_barrier_wait_gives_up_and_context_recovers(Sim):
     ref, _ = O.forward(g, 400)
     _check_v(tr, ref)
     s.close()
+
+
+def test_requested_gradient_kinds_only(Sim):
+    """hx_set_grad_kinds: the reverse sweep accumulates only the requested
+    kinds; those equal the all-kinds gradients bit for bit (each accumulator's
+    arithmetic is its own), the others read as zero, and resetting restores
+    all kinds."""
+    g = synth.spiking_network(ncell=6, seed=21, nstim=4, weight=(0.02, 0.08), stim_noise=1.0, stim_interval=5.0)
+    T = 1200
+    s = Sim(0)
+    s.load_group(g)
+    p = g.soma_nodes()
+    c = np.random.default_rng(3).standard_normal((T + 1, p.shape[0]))
+    s.forward_capture(T, probes=p)
+    full = s.backward(c)
+    want = ("hh.gnabar", "Exp2Syn.weight")
+    s.set_grad_kinds(want)
+    part = s.backward(c)
+    for k in part:
+        if k in want or (k == "ExpSyn.weight"):  # ExpSyn and Exp2Syn weights share one accumulator
+            assert np.array_equal(part[k], full[k]), k
+        elif k in GRAD_KINDS + NET_KINDS:
+            assert not np.any(part[k]), k
+    assert np.max(np.abs(full["hh.gnabar"])) > 0 and np.max(np.abs(full["Exp2Syn.weight"])) > 0
+    s.set_grad_kinds(None)
+    again = s.backward(c)
+    for k in full:
+        assert np.array_equal(again[k], full[k]), k
+    s.close()
