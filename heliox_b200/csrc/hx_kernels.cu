@@ -227,8 +227,15 @@ __global__ void __launch_bounds__(kThreads, 1) fwd_kernel(DevGroup G, DevState S
                         if (write_tape) N.tS[(size_t)(k - T.k_base + 1) * N.ngr + j] = sj;
                     }
                 }
-                assemble<true, true, false, false, kCpl>(G, M, pb, i, fl, q, vi, sv, sa, sb, gm, gh, gn, tm, r, dd, N,
-                                                         N.sA, N.sB, sp, N.gr_s, vpeer);
+                if (kLib) {  // library channels after the network mechanisms (CoreNEURON type order)
+                    double ica;
+                    assemble<true, true, false, true, kCpl>(G, M, pb, i, fl, q, vi, sv, sa, sb, gm, gh, gn, tm, r, dd,
+                                                            N, N.sA, N.sB, sp, N.gr_s, vpeer, &L, L.st, &ica);
+                    L.nica[pb + i] = ica;
+                } else {
+                    assemble<true, true, false, false, kCpl>(G, M, pb, i, fl, q, vi, sv, sa, sb, gm, gh, gn, tm, r,
+                                                             dd, N, N.sA, N.sB, sp, N.gr_s, vpeer);
+                }
             } else if (kLib) {
                 double ica;
                 assemble<true, false, false, true>(G, M, pb, i, fl, q, vi, sv, sa, sb, gm, gh, gn, tm, r, dd, N,
@@ -441,8 +448,16 @@ __global__ void __launch_bounds__(kThreads, 1) bwd_kernel(DevGroup G, DevTape T,
                 SynPre sp;
                 load_syn(N, nx, tA, tB, sp);
                 syn_next(G, N, M, pb, i + g.nt, i1, nx);
-                assemble<false, true, false, false, kCpl>(G, M, pb, i, fl, q, vk, nullptr, sa, sb, gm, gh, gn, tm, r,
-                                                          dd, N, tA, tB, sp, grs, vpeer);
+                if (kLib) {
+                    const double* Xk = L.tape + (size_t)(k - L.k_base) * (size_t)L.nst;
+                    double ica;
+                    assemble<false, true, false, true, kCpl>(G, M, pb, i, fl, q, vk, nullptr, sa, sb, gm, gh, gn, tm,
+                                                             r, dd, N, tA, tB, sp, grs, vpeer, &L, Xk, &ica);
+                    mu += lib::lib_state_adj(L, pb + i, T.v[off + G.nnode + i], Xk, Xk + L.nst, ica);
+                } else {
+                    assemble<false, true, false, false, kCpl>(G, M, pb, i, fl, q, vk, nullptr, sa, sb, gm, gh, gn, tm,
+                                                              r, dd, N, tA, tB, sp, grs, vpeer);
+                }
             } else if (kLib) {
                 const double* Xk = L.tape + (size_t)(k - L.k_base) * (size_t)L.nst;
                 double ica;
@@ -745,11 +760,25 @@ cudaError_t configure_kernels(size_t smem_fwd, size_t smem_bwd, size_t smem_fwd_
     e = cudaFuncSetAttribute(bwd_kernel<true, false, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              (int)smem_bwd_net);
     if (e != cudaSuccess) return e;
+    e = cudaFuncSetAttribute(fwd_kernel<true, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_fwd_net);
+    if (e != cudaSuccess) return e;
+    e = cudaFuncSetAttribute(bwd_kernel<true, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_bwd_net);
+    if (e != cudaSuccess) return e;
+    e = cudaFuncSetAttribute(fwd_kernel<true, true, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)smem_fwd_net);
+    if (e != cudaSuccess) return e;
+    e = cudaFuncSetAttribute(bwd_kernel<true, true, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)smem_bwd_net);
+    if (e != cudaSuccess) return e;
     return cudaFuncSetAttribute(bwd_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_bwd_net);
 }
 
-const void* fwd_cpl_kernel_ptr() { return (const void*)fwd_kernel<true, false, true>; }
-const void* bwd_cpl_kernel_ptr() { return (const void*)bwd_kernel<true, false, true>; }
+const void* fwd_cpl_kernel_ptr(bool lib) {
+    return lib ? (const void*)fwd_kernel<true, true, true> : (const void*)fwd_kernel<true, false, true>;
+}
+const void* bwd_cpl_kernel_ptr(bool lib) {
+    return lib ? (const void*)bwd_kernel<true, true, true> : (const void*)bwd_kernel<true, false, true>;
+}
 
 cudaError_t launch_init(const DevGroup& G, const DevState& S, double v_init, cudaStream_t st) {
     init_state_kernel<<<(G.nnode + 255) / 256, 256, 0, st>>>(G, S, v_init);
@@ -766,16 +795,29 @@ cudaError_t launch_fwd(const DevGroup& G, const DevState& S, const DevTape& T, i
                        double* trace, const double* tmid, int k0, int k1, cudaStream_t st, const DevNet* N,
                        const DevLib* L) {
     if (N) {
+        DevLib Lc{};
+        if (L) {
+            Lc = *L;
+            Lc.k_base = T.k_base;
+        }
         if (N->coupled && N->gsync) {  // every pack co-resident: one cooperative launch for the window
             DevGroup Gc = G;
             DevState Sc = S;
             DevTape Tc = T;
             DevProbe Pc = P;
             DevNet Nc = *N;
-            DevLib Lc{};
             void* args[] = {&Gc, &Sc, &Tc, &write_tape, &Pc, &trace, &tmid, &k0, &k1, &Nc, &Lc};
-            return cudaLaunchCooperativeKernel((const void*)fwd_kernel<true, false, true>, dim3(G.npack),
-                                               dim3(kThreads), args, fwd_smem_bytes(G), st);
+            const void* f = L ? (const void*)fwd_kernel<true, true, true> : (const void*)fwd_kernel<true, false, true>;
+            return cudaLaunchCooperativeKernel(f, dim3(G.npack), dim3(kThreads), args, fwd_smem_bytes(G), st);
+        }
+        if (L) {  // library mechanisms in a network group
+            if (N->coupled)
+                fwd_kernel<true, true, true><<<G.npack, kThreads, fwd_smem_bytes(G), st>>>(G, S, T, write_tape, P, trace,
+                                                                                       tmid, k0, k1, *N, Lc);
+            else
+                fwd_kernel<true, true><<<G.npack, kThreads, fwd_smem_bytes(G), st>>>(G, S, T, write_tape, P, trace, tmid,
+                                                                                   k0, k1, *N, Lc);
+            return cudaGetLastError();
         }
         if (N->coupled)
             fwd_kernel<true, false, true><<<G.npack, kThreads, fwd_smem_bytes(G), st>>>(G, S, T, write_tape, P, trace,
@@ -799,6 +841,11 @@ cudaError_t launch_bwd(const DevGroup& G, const DevTape& T, const DevAdj& A, con
                        const double* dLdv, const double* tmid, int k_hi, int k_lo, cudaStream_t st, const DevNet* N,
                        const DevLib* L) {
     if (N) {
+        DevLib Lc{};
+        if (L) {
+            Lc = *L;
+            Lc.k_base = T.k_base;
+        }
         if (N->coupled && N->gsync) {
             DevGroup Gc = G;
             DevTape Tc = T;
@@ -806,10 +853,18 @@ cudaError_t launch_bwd(const DevGroup& G, const DevTape& T, const DevAdj& A, con
             DevGrad GRc = GR;
             DevProbe Pc = P;
             DevNet Nc = *N;
-            DevLib Lc{};
             void* args[] = {&Gc, &Tc, &Ac, &GRc, &Pc, &dLdv, &tmid, &k_hi, &k_lo, &Nc, &Lc};
-            return cudaLaunchCooperativeKernel((const void*)bwd_kernel<true, false, true>, dim3(G.npack),
-                                               dim3(kThreads), args, bwd_smem_bytes(G), st);
+            const void* f = L ? (const void*)bwd_kernel<true, true, true> : (const void*)bwd_kernel<true, false, true>;
+            return cudaLaunchCooperativeKernel(f, dim3(G.npack), dim3(kThreads), args, bwd_smem_bytes(G), st);
+        }
+        if (L) {
+            if (N->coupled)
+                bwd_kernel<true, true, true><<<G.npack, kThreads, bwd_smem_bytes(G), st>>>(G, T, A, GR, P, dLdv, tmid,
+                                                                                       k_hi, k_lo, *N, Lc);
+            else
+                bwd_kernel<true, true><<<G.npack, kThreads, bwd_smem_bytes(G), st>>>(G, T, A, GR, P, dLdv, tmid, k_hi,
+                                                                                   k_lo, *N, Lc);
+            return cudaGetLastError();
         }
         if (N->coupled)
             bwd_kernel<true, false, true><<<G.npack, kThreads, bwd_smem_bytes(G), st>>>(G, T, A, GR, P, dLdv, tmid, k_hi,

@@ -13,12 +13,13 @@ size_t split_fwd_smem_bytes(const DevGroup& G);
 size_t split_bwd_smem_bytes(const DevGroup& G);
 cudaError_t configure_kernels(size_t smem_fwd, size_t smem_bwd, size_t smem_fwd_net, size_t smem_bwd_net);
 // the coupled-network instantiations (occupancy checks of grid-synchronous launches)
-const void* fwd_cpl_kernel_ptr();
-const void* bwd_cpl_kernel_ptr();
+const void* fwd_cpl_kernel_ptr(bool lib);
+const void* bwd_cpl_kernel_ptr(bool lib);
 cudaError_t launch_init(const DevGroup& G, const DevState& S, double v_init, cudaStream_t st);
 cudaError_t launch_lib_init(const DevLib& L, int nnode, double v_init, cudaStream_t st);
 // N and L null: the plain kernels; N: the network instantiation; L: the
-// library-mechanism instantiation (its tape rows are counted from T.k_base)
+// library-mechanism instantiation (its tape rows are counted from T.k_base);
+// both: library mechanisms in a network group
 cudaError_t launch_fwd(const DevGroup& G, const DevState& S, const DevTape& T, int write_tape, const DevProbe& P,
                        double* trace, const double* tmid, int k0, int k1, cudaStream_t st, const DevNet* N = nullptr,
                        const DevLib* L = nullptr);

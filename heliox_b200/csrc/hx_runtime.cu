@@ -545,9 +545,9 @@ int hx_load_group(hx_ctx* ctx, const hx_group_desc* desc) {
     if (ctx->coupled && !ctx->split) {
         int coop = 0, per_f = 0, per_b = 0;
         HXC(cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, ctx->device));
-        HXC(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_f, hx::fwd_cpl_kernel_ptr(), hx::kThreads,
+        HXC(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_f, hx::fwd_cpl_kernel_ptr(ctx->lib), hx::kThreads,
                                                           std::min(sfn, (size_t)maxsmem)));
-        HXC(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_b, hx::bwd_cpl_kernel_ptr(), hx::kThreads,
+        HXC(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_b, hx::bwd_cpl_kernel_ptr(ctx->lib), hx::kThreads,
                                                           std::min(sbn, (size_t)maxsmem)));
         ctx->gsync_fit = coop && (long long)std::min(per_f, per_b) * nsm >= P.npack;
     }

@@ -150,7 +150,6 @@ int hx_lib_load(hx_ctx* ctx, const hx_group_desc* desc) {
         }
         return 0;
     }
-    if (ctx->net) return fail(ctx, "library mechanisms cannot be combined with network parts");
     const hx::Plan& P = ctx->P;
     const int nn = P.nnode;
     // reference node -> instance of each type

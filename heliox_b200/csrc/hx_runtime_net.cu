@@ -369,8 +369,17 @@ static int net_window(const hx_ctx* c, int nstep) {
     return std::max(1, std::min(W, std::max(nstep, 1)));
 }
 
-// one checkpoint: v, m, h, n, then synapse A, B and graded s
+// one checkpoint: v, m, h, n, then synapse A, B and graded s (library
+// states in lib_ck)
 static int net_ck(hx_ctx* ctx, int s, bool save, double* vsrc) {
+    if (ctx->lib && ctx->lib_nst) {
+        const size_t nls = (size_t)ctx->lib_nst;
+        double* lb = ctx->lib_ck.p + nls * (size_t)s;
+        if (save)
+            HXC(cudaMemcpyAsync(lb, ctx->lib_st.p, nls * 8, cudaMemcpyDeviceToDevice, ctx->st));
+        else
+            HXC(cudaMemcpyAsync(ctx->lib_st.p, lb, nls * 8, cudaMemcpyDeviceToDevice, ctx->st));
+    }
     const size_t nn = ctx->P.nnode;
     const size_t stride = 4 * nn + ctx->ck_net_stride;
     double* base = ctx->ck.p + stride * (size_t)s;
@@ -392,8 +401,8 @@ static int net_ck(hx_ctx* ctx, int s, bool save, double* vsrc) {
 // W: the forward window; a free window (no synapses, no window set by the
 // caller) follows the checkpoint segment instead
 static int net_plan_tape(hx_ctx* ctx, int nstep, int& W) {
-    const size_t nn = ctx->P.nnode, ns = ctx->nsyn, ng = ctx->ngr;
-    const size_t per_step = (4 * nn + 2 * ns + ng) * sizeof(double);
+    const size_t nn = ctx->P.nnode, ns = ctx->nsyn, ng = ctx->ngr, nls = ctx->lib ? (size_t)ctx->lib_nst : 0;
+    const size_t per_step = (4 * nn + 2 * ns + ng + nls) * sizeof(double);
     size_t budget = ctx->tape_budget;
     if (!budget) {
         size_t fr = 0, tot = 0;
@@ -408,7 +417,9 @@ static int net_plan_tape(hx_ctx* ctx, int nstep, int& W) {
         HXC(ctx->tA.ensure(std::max<size_t>(ns * rows, 1)));
         HXC(ctx->tB.ensure(std::max<size_t>(ns * rows, 1)));
         HXC(ctx->tS.ensure(std::max<size_t>(ng * (rows + 1), 1)));
+        if (nls) HXC(ctx->lib_tape.ensure(nls * rows));
         if (ckn) HXC(ctx->ck.ensure((4 * nn + ctx->ck_net_stride) * ckn));
+        if (ckn && nls) HXC(ctx->lib_ck.ensure(nls * ckn));
         return 0;
     };
     if (per_step * (size_t)(nstep + 2) <= budget) {
@@ -526,6 +537,7 @@ int hx_net_forward(hx_ctx* ctx, int nstep, double v_init, double* trace_dev, boo
             if (ctx->N.gsync) HXC(cudaMemsetAsync(ctx->gs_err.p, 0, 4, st));
             double* v0 = ctx->coupled ? ctx->vbuf.p : ctx->sv.p;
             HXC(hx::launch_init(ctx->G, hx::DevState{v0, ctx->sm.p, ctx->sh.p, ctx->sn.p}, v_init, st));
+            if (ctx->lib) HXC(hx::launch_lib_init(ctx->L, (int)nn, v_init, st));
             HXC(hx::launch_init_net(ctx->nsyn, ctx->sA.p, ctx->sB.p, ctx->ngr, ctx->prm[HX_P_GRADED_W].p,
                                     ctx->gr_vth.p, ctx->gr_delta.p, ctx->gr_g.p, ctx->gr_k.p, ctx->gr_erev.p,
                                     ctx->gr_s.p, v_init, st));
@@ -567,7 +579,10 @@ int hx_net_forward(hx_ctx* ctx, int nstep, double v_init, double* trace_dev, boo
                 HXC(cudaMemsetAsync(ctx->gs_bar.p, 0, 2 * sizeof(unsigned), st));
             }
             hx::DevState S{vin, ctx->sm.p, ctx->sh.p, ctx->sn.p};
-            HXC(hx::launch_fwd(ctx->G, S, T, write_tape, PV, trace_dev, ctx->tmid.p, k0, k1, st, &N));
+            hx::DevLib Lv = ctx->L;
+            Lv.tape = ctx->lib_tape.p;
+            HXC(hx::launch_fwd(ctx->G, S, T, write_tape, PV, trace_dev, ctx->tmid.p, k0, k1, st, &N,
+                               ctx->lib ? &Lv : nullptr));
             HXC(hx::launch_log_append(ctx->win_send.p, ctx->win_n.p, ctx->win_cap, ctx->spk_log.p, ctx->log_n.p,
                                       ctx->log_cap, ctx->dev_err.p, ctx->win_max.p, st));
             launches += 2;
@@ -679,6 +694,10 @@ int hx_net_backward(hx_ctx* ctx, const double* dLdv_dev) {
         HXC(cudaMemsetAsync(ctx->lB.p, 0, (size_t)ctx->nsyn * 8, st));
     }
     if (ctx->ngr) HXC(cudaMemsetAsync(ctx->lS.p, 0, (size_t)ctx->ngr * 8, st));
+    if (ctx->lib && ctx->lib_nst) HXC(cudaMemsetAsync(ctx->lib_lam.p, 0, (size_t)ctx->lib_nst * 8, st));
+    hx::DevLib Lv = ctx->L;
+    Lv.tape = ctx->lib_tape.p;
+    const hx::DevLib* LP = ctx->lib ? &Lv : nullptr;
     if (ctx->coupled) HXC(cudaMemsetAsync(ctx->xbuf.p, 0, 2 * std::max<size_t>(nx, 1) * 8, st));
     const bool gsync = ctx->coupled && ctx->N.gsync;
     if (gsync) HXC(cudaMemsetAsync(ctx->gs_err.p, 0, 4, st));
@@ -716,11 +735,11 @@ int hx_net_backward(hx_ctx* ctx, const double* dLdv_dev) {
         if (hx_kev_mark(ctx, st)) return -1;
         if (!ctx->coupled || gsync) {
             if (gsync) HXC(cudaMemsetAsync(ctx->gs_bar.p, 0, 2 * sizeof(unsigned), st));
-            HXC(hx::launch_bwd(ctx->G, T, A, GR, PV, dLdv_dev, ctx->tmid.p, k_hi, k_lo, st, &N));
+            HXC(hx::launch_bwd(ctx->G, T, A, GR, PV, dLdv_dev, ctx->tmid.p, k_hi, k_lo, st, &N, LP));
         } else {
             for (int k = k_hi - 1; k >= k_lo; --k) {
                 set_x(k);
-                HXC(hx::launch_bwd(ctx->G, T, A, GR, PV, dLdv_dev, ctx->tmid.p, k + 1, k, st, &N));
+                HXC(hx::launch_bwd(ctx->G, T, A, GR, PV, dLdv_dev, ctx->tmid.p, k + 1, k, st, &N, LP));
             }
         }
         if (hx_kev_mark(ctx, st)) return -1;
@@ -741,7 +760,7 @@ int hx_net_backward(hx_ctx* ctx, const double* dLdv_dev) {
             if (!ctx->coupled) {
                 if (net_ck(ctx, s, false, ctx->sv.p)) return -1;
                 hx::DevState S{ctx->sv.p, ctx->sm.p, ctx->sh.p, ctx->sn.p};
-                HXC(hx::launch_fwd(ctx->G, S, T, 1, PV, nullptr, ctx->tmid.p, k0, k1, st, &N));
+                HXC(hx::launch_fwd(ctx->G, S, T, 1, PV, nullptr, ctx->tmid.p, k0, k1, st, &N, LP));
                 launches++;
             } else if (gsync) {  // the segment's recompute in one grid-synchronous launch
                 double* vin = ctx->vbuf.p + (size_t)(k0 & 1) * nn;
@@ -751,7 +770,7 @@ int hx_net_backward(hx_ctx* ctx, const double* dLdv_dev) {
                 NF.vout = ctx->vbuf.p + (size_t)(k1 & 1) * nn;
                 hx::DevState S{vin, ctx->sm.p, ctx->sh.p, ctx->sn.p};
                 HXC(cudaMemsetAsync(ctx->gs_bar.p, 0, 2 * sizeof(unsigned), st));
-                HXC(hx::launch_fwd(ctx->G, S, T, 1, PV, nullptr, ctx->tmid.p, k0, k1, st, &NF));
+                HXC(hx::launch_fwd(ctx->G, S, T, 1, PV, nullptr, ctx->tmid.p, k0, k1, st, &NF, LP));
                 launches++;
             } else {
                 if (net_ck(ctx, s, false, ctx->vbuf.p + (size_t)(k0 & 1) * nn)) return -1;
@@ -760,7 +779,7 @@ int hx_net_backward(hx_ctx* ctx, const double* dLdv_dev) {
                     NF.vpeer = ctx->vbuf.p + (size_t)(k & 1) * nn;
                     NF.vout = ctx->vbuf.p + (size_t)((k + 1) & 1) * nn;
                     hx::DevState S{const_cast<double*>(NF.vpeer), ctx->sm.p, ctx->sh.p, ctx->sn.p};
-                    HXC(hx::launch_fwd(ctx->G, S, T, 1, PV, nullptr, ctx->tmid.p, k, k + 1, st, &NF));
+                    HXC(hx::launch_fwd(ctx->G, S, T, 1, PV, nullptr, ctx->tmid.p, k, k + 1, st, &NF, LP));
                     launches++;
                 }
             }

@@ -448,7 +448,8 @@ def _cell_nodes(g: CellGroup) -> List[np.ndarray]:
 def spiking_network(ncell: int = 8, seed: int = 11, nmin: int = 40, nmax: int = 120, syn_per_cell: int = 6,
                     nstim: int = 4, exp_frac: float = 0.3, weight: Tuple[float, float] = (0.005, 0.03),
                     delay: Tuple[float, float] = (1.0, 5.0), drive_frac: float = 0.5,
-                    stim_interval: float = 8.0, stim_number: float = 20.0, stim_noise: float = 0.5) -> CellGroup:
+                    stim_interval: float = 8.0, stim_number: float = 20.0, stim_noise: float = 0.5,
+                    cell=None) -> CellGroup:
     """A small event-driven network of random-tree cells (test scale).
 
     Every cell receives ``syn_per_cell`` synapses at uniformly drawn nodes of
@@ -458,10 +459,12 @@ def spiking_network(ncell: int = 8, seed: int = 11, nmin: int = 40, nmax: int = 
     delay U[delay] and weight U[weight] uS.  ``nstim`` NetStims (interval,
     number, start 1 ms, noise) each drive one extra Exp2Syn at the soma of
     cell ``i % ncell``.  Only a fraction ``drive_frac`` of the cells keep
-    their somatic IClamp.
+    their somatic IClamp.  ``cell(seed, nmin, nmax)`` builds each cell
+    (default ``random_tree_cell``; ``lib_network`` passes library cells).
     """
     rng = np.random.default_rng(seed)
-    cells = [random_tree_cell(seed * 1000 + c, nmin=nmin, nmax=nmax) for c in range(ncell)]
+    make = cell or (lambda sd, lo, hi: random_tree_cell(sd, nmin=lo, nmax=hi))
+    cells = [make(seed * 1000 + c, nmin, nmax) for c in range(ncell)]
     g = concat_groups(cells, name=f"net{ncell}")
     amp = g.iclamp.fields["amp"].copy()
     amp[rng.random(amp.shape[0]) >= drive_frac] = 0.0
@@ -578,7 +581,7 @@ def network_config4_shard(total: int, rank: int, nranks: int, seed: int = 4, syn
 def coupled_network(ncell: int = 6, seed: int = 5, nmin: int = 50, nmax: int = 150, ngap: int = 6,
                     ngapj: int = 3, ngraded: int = 10, drive_frac: float = 0.4,
                     gap_g: Tuple[float, float] = (1e-4, 1e-3), graded_w: Tuple[float, float] = (2e-4, 2e-3),
-                    ngapnp: int = 0) -> CellGroup:
+                    ngapnp: int = 0, cell=None) -> CellGroup:
     """Config 5 style network: cells coupled by gap junctions and graded synapses.
 
     ``ngap`` HalfGap pairs (two instances per pair at random nodes of two
@@ -589,10 +592,12 @@ def coupled_network(ncell: int = 6, seed: int = 5, nmin: int = 50, nmax: int = 1
     Vth -20 mV, the MOD defaults otherwise), ``ngapnp`` gapjunction_noptr
     pairs (weight U[gap_g], vpre from the partner node; drawn after the others,
     so the rest of the network does not depend on it).  A fraction
-    ``drive_frac`` of the cells keep their somatic IClamp.
+    ``drive_frac`` of the cells keep their somatic IClamp.  ``cell`` as in
+    ``spiking_network``.
     """
     rng = np.random.default_rng(seed)
-    cells = [random_tree_cell(seed * 1000 + c, nmin=nmin, nmax=nmax) for c in range(ncell)]
+    make = cell or (lambda sd, lo, hi: random_tree_cell(sd, nmin=lo, nmax=hi))
+    cells = [make(seed * 1000 + c, nmin, nmax) for c in range(ncell)]
     g = concat_groups(cells, name=f"coupled{ncell}")
     amp = g.iclamp.fields["amp"].copy()
     amp[rng.random(amp.shape[0]) >= drive_frac] = 0.0
@@ -643,6 +648,24 @@ def coupled_network(ncell: int = 6, seed: int = 5, nmin: int = 50, nmax: int = 1
                            "Vth": np.full(ng, -20.0), "erev": np.full(ng, 30.0), "dvpre": np.full(ng, 1e-3)},
                       {"pre": rp})
     g.validate()
+    return g
+
+
+def lib_network(kind: str = "event", ncell: int = 6, seed: int = 41, channels=None, cadyn: str = "CaDynamics_E2",
+                **kw) -> CellGroup:
+    """A network of library cells (``lib_tree_cell``: the channel set, ions,
+    calcium dynamics): ``kind`` "event" wires them like ``spiking_network``
+    (ExpSyn / Exp2Syn, NetCons, NetStims), "coupled" like ``coupled_network``
+    (HalfGap, gapjunction_lr / _noptr, graded synapses) -- the worm networks
+    with learned channels of the reference's worm-lr set."""
+    def make(sd, lo, hi):
+        return lib_tree_cell(sd, nmin=lo, nmax=hi, channels=channels, cadyn=cadyn)
+
+    kw.setdefault("nmin", 60)
+    kw.setdefault("nmax", 140)
+    g = (spiking_network if kind == "event" else coupled_network)(ncell=ncell, seed=seed, cell=make, **kw)
+    g.v_init = -75.0
+    g.name = f"lib{kind}{ncell}"
     return g
 
 

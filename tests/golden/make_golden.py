@@ -36,6 +36,9 @@ CASES = {
     # gapjunction_noptr (vpre through the gap transfer) on nodes that also carry
     # HalfGap, gapjunction_lr and graded synapses: the per-node current order
     "net_gapnoptr": (lambda: net_gapnoptr(), 2000, None),
+    # library cells (channels, ions, calcium dynamics) coupled by gaps and graded synapses
+    "lib_net_coupled": (lambda: synth.lib_network("coupled", ncell=5, seed=44, ngap=4, ngapj=3, ngraded=8,
+                                                  ngapnp=3), 1600, None),
     # user-mech channel set with calcium dynamics (spiking library cells)
     "lib_cells": (lambda: synth.lib_tree_batch(2, seed0=700, nmax=200), 2000, None),
     # hh cells and library cells in one group

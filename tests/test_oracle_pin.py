@@ -177,6 +177,23 @@ def test_network_adjoint_vs_fd_of_reference_forward():
 
 
 @needs_ref
+@pytest.mark.parametrize("kind", ["event", "coupled"])
+def test_oracle_library_networks_bit_exact_vs_reference_live(kind):
+    """Library cells in an event network and in a coupled network (HalfGap,
+    gapjunction_lr / _noptr, graded synapses): the network currents before
+    the library ones on a node, as the reference's mechanism list orders them."""
+    if kind == "event":
+        g = synth.lib_network("event", ncell=5, seed=43, nstim=3, weight=(0.02, 0.08), stim_noise=1.0,
+                              stim_interval=5.0)
+    else:
+        g = synth.lib_network("coupled", ncell=5, seed=44, ngap=4, ngapj=3, ngraded=8, ngapnp=3)
+    p = np.arange(g.nnode, dtype=np.int32)[::7]
+    ref, _ = O.ref_forward(g, 1600, probe=p)
+    ora, _ = O.forward(g, 1600, probe=p)
+    assert np.array_equal(ref, ora)
+
+
+@needs_ref
 @pytest.mark.parametrize("seed,cadyn", [(1, "CaDynamics_E2"), (2, "CaDynamics_E2"), (3, "cainternm_lr")])
 def test_oracle_library_cells_bit_exact_vs_reference_live(seed, cadyn):
     """The library channel set, ions and calcium dynamics (CaDynamics_E2 or
