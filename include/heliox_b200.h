@@ -205,8 +205,8 @@ typedef struct hx_group_desc {
     const int *gr_node, *gr_pre;
     const double *gr_w, *gr_delta, *gr_vth;
 
-    /* ---- library mechanisms (NULL = none; not combined with network parts
-     * or a cell split across CTAs) */
+    /* ---- library mechanisms (NULL = none; not on a cell split across CTAs;
+     * with network parts their currents follow the network mechanisms') */
     const hx_lib_desc* lib;
 } hx_group_desc;
 
