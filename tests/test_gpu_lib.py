@@ -199,7 +199,7 @@ def _fd_view(g, key, u, T, probes, c, h):
     return (-vals[0] + 8 * vals[1] - 8 * vals[2] + vals[3]) / (12 * h)
 
 
-@pytest.mark.parametrize("kind,tape_budget", [("event", 0), ("coupled", 0), ("event", 2 << 20)])
+@pytest.mark.parametrize("kind,tape_budget", [("event", 0), ("coupled", 0), ("event", 24 << 20)])
 def test_library_cells_in_networks(Sim, kind, tape_budget):
     """Library cells wired into an event network (ExpSyn / Exp2Syn, NetStims)
     or a coupled one (HalfGap, gapjunction_lr / _noptr, graded synapses; the
