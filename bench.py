@@ -50,9 +50,10 @@ NCELL_NET = 10000
 SEED0 = 20240
 # DRAM bytes per compartment-step of the network reverse kernel, measured by
 # ncu (dram__bytes_read.sum + dram__bytes_write.sum of one bwd_kernel launch
-# over 1250 config-4 cells x 200 steps, / its compartment-steps); scaled to a
-# launch of the timed configuration as roofline.traffic (config 4 only)
-REV_DRAM_BYTES_PER_UNIT_NET = 409.1
+# over 1250 config-4 cells x 200 steps with this bench's gradient kinds, / its
+# compartment-steps); scaled to a launch of the timed configuration as
+# roofline.traffic (config 4 only)
+REV_DRAM_BYTES_PER_UNIT_NET = 209.9
 
 
 def _alg_bytes(g):
