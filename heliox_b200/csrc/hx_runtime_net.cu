@@ -429,7 +429,8 @@ static int net_plan_tape(hx_ctx* ctx, int nstep, int& W) {
         return alloc((size_t)nstep + 1, 0);
     }
     // segments of K steps, K a multiple of the window
-    const bool free_window = ctx->nsyn == 0 && ctx->window_user <= 0;
+    // (ranks that exchange windows keep the one window they agreed on)
+    const bool free_window = ctx->nsyn == 0 && ctx->window_user <= 0 && !(ctx->exchange && ctx->nranks > 1);
     if (free_window) W = 1;
     size_t K = (size_t)std::sqrt((double)nstep);
     K = std::max<size_t>(W, (K + W - 1) / W * W);
