@@ -177,6 +177,24 @@ def test_network_adjoint_vs_fd_of_reference_forward():
 
 
 @needs_ref
+@pytest.mark.parametrize("case", ["trees3", "tree_deep", "net_spiking"])
+def test_oracle_vs_reference_permute1_live(case):
+    """The reference with permute type 1 (cpu_solve_permute1,
+    simulate.cpp:583-629: the node order of permute_order.cpp's type-1 split)
+    eliminates in another order than solve_serial: it agrees with the
+    serial-order oracle to rounding (measured 1e-13 .. 3e-13 of the trace
+    scale), spikes identical."""
+    make, nstep, _ = _mg.CASES[case]
+    g = make()
+    p = g.soma_nodes()
+    ref, rs = O.ref_forward(g, nstep, probe=p, permute_type=1)
+    ora, st = O.forward(g, nstep, probe=p)
+    assert np.max(np.abs(ref - ora)) / np.max(np.abs(ora)) <= 1e-9
+    if g.has_network:
+        assert [gid for _, gid in sorted(st["spikes"])] == [int(gid) for _, gid in rs]
+
+
+@needs_ref
 @pytest.mark.parametrize("kind", ["event", "coupled"])
 def test_oracle_library_networks_bit_exact_vs_reference_live(kind):
     """Library cells in an event network and in a coupled network (HalfGap,
