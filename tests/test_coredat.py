@@ -46,6 +46,8 @@ def _same(g, h):
         lambda: synth.spiking_network(),
         lambda: synth.coupled_network(),
         lambda: synth.coupled_network(ncell=4, seed=9, ngapnp=4),
+        lambda: synth.lib_network("coupled", ncell=4, seed=10, ngap=3, ngapj=2, ngraded=5, ngapnp=2),
+        lambda: synth.lib_network("event", ncell=4, seed=11, nstim=2),
         lambda: synth.lib_tree_batch(2, seed0=8, nmax=150),
         lambda: synth.lib_tree_batch(2, seed0=9, nmax=150, cadyn="cainternm_lr"),
         lambda: _lib_mixed(),
