@@ -132,7 +132,7 @@ struct DevNet {
     int ngr;
     double *gr_s, *lS;  // state s (s_{k-1} entering step k), adjoint of s
     double* tS;         // tape: row 0 = s_{k_base-1}, row k-k_base+1 = s_k
-    int coupled;             // gaps or graded synapses present: one step per launch
+    int coupled;             // gaps or graded synapses present: partner voltages every step
     const double* vpeer;     // v_k of every node (read-only during a coupled launch)
     double* vout;            // v_{k+1} written by a coupled forward launch
     // reverse-sweep coupling: per-instance contributions to the partner's

@@ -8,8 +8,11 @@
 // the caller's exchange hook, and routed into per-step event buckets.  NetStim
 // trains do not depend on any voltage: they are generated on the host once
 // per forward length (hx_netstim.cpp) and routed before the first window.
-// Groups coupled by gap junctions or graded synapses advance one step per
-// launch, partner voltages passing through a ping-pong buffer.
+// Groups coupled by gap junctions or graded synapses exchange partner
+// voltages every step through a ping-pong buffer: a window is one
+// cooperative launch with a grid barrier per step when every pack can be
+// co-resident, else one launch per step.  Library mechanisms may sit in
+// network groups (the kNet + kLib instantiations).
 //
 // Backward: the event schedule of the forward is held fixed; the reverse
 // sweep reads the synapse states after each step's deliveries from the tape
