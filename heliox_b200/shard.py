@@ -47,7 +47,8 @@ def shard(g: CellGroup, nranks: int, rank: int) -> Tuple[CellGroup, int, int]:
     order (roots first), its synapses with global NetCon sources, the whole
     NetStim table; ``gid_base`` is the global id of its first cell and
     ``nsrc_cells`` the number of cells over all shards.  The group's
-    ``meta["global_index"]`` maps its synapse instances to the network's.
+    ``meta["global_index"]`` maps its synapse and library-mechanism instances
+    to the network's.
     """
     if g.coupled:
         raise ValueError("gap junctions and graded synapses are not partitioned across ranks")
@@ -92,6 +93,7 @@ def shard(g: CellGroup, nranks: int, rank: int) -> Tuple[CellGroup, int, int]:
         netstim=g.netstim.copy(),
         ps_thresh=_f64(g.ps_thresh[c0:c1]),
         netstim_rng=g.netstim_rng,
+        lib={nm: sub(tab, nm) for nm, tab in g.lib.items()},
     )
     # instance i of the shard's ExpSyn / Exp2Syn table is global instance
     # meta["global_index"][mech][i]

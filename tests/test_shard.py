@@ -37,6 +37,23 @@ def test_shards_cover_the_network(nranks):
     assert allsyn == sorted(zip(g.exp2syn.ifields["src"].tolist(), g.exp2syn.fields["weight"].tolist()))
 
 
+@pytest.mark.parametrize("nranks", [2, 3])
+def test_shards_carry_library_mechanisms(nranks):
+    """Library cells in an event network: every library table is partitioned
+    with its cells (instance counts add up, each instance's fields travel with
+    it, global_index maps back), and every shard is a valid group."""
+    g = synth.lib_network("event", ncell=5, seed=12, nstim=2)
+    parts = [shard.shard(g, nranks, r) for r in range(nranks)]
+    for nm, tab in g.lib.items():
+        assert sum(p.lib[nm].n for p, _, _ in parts) == tab.n, nm
+        for p, _, _ in parts:
+            gi = p.meta["global_index"][nm]
+            for k, v in p.lib[nm].fields.items():
+                assert np.array_equal(v, tab.fields[k][gi]), (nm, k)
+    for p, _, _ in parts:
+        p.validate()
+
+
 def test_shard_rejects_coupled_networks():
     with pytest.raises(ValueError):
         shard.shard(synth.coupled_network(ncell=4), 2, 0)
