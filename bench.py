@@ -7,7 +7,9 @@ pas, somatic IClamp), 100 Exp2Syn per cell from random presynaptic cells plus
 one NetStim-driven Exp2Syn (5 Hz, noise 1), 8000 steps of dt 0.025 ms.  One
 step = forward with checkpointed tape, soma-voltage MSE against a teacher
 network (weights perturbed lognormally, sigma 0.2), and the reverse sweep
-producing every synaptic weight gradient.  On N GPUs the SAME network is
+producing the gradients of every synaptic weight and every hh gnabar (the
+kinds the bench asks for; the sweep accumulates only those).  On N GPUs the
+SAME network is
 sharded by cell (strong scaling); after every minimum-delay window the ranks
 all-gather their window spikes over NCCL.
 
